@@ -1,0 +1,114 @@
+/*
+ * cb_oracle.h -- CPU restatement of catboost_rs's oblivious-tree training path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This library is the parity checker for the CUDA
+ * implementation in catboost_rs_b200/csrc and the CPU baseline timed by
+ * bench.py.  Nothing in the product path links, loads or calls it.
+ *
+ * Every routine restates the reference's CPU algorithm in plain C with the
+ * same floating-point operation order (strict left-to-right f64 sums, no FMA
+ * contraction: build with -ffp-contract=off).  Citations are file:line inside
+ * the reference project (BectorVoom/catboost_rs).
+ *
+ * Parity status: pinned.  tests/test_oracle_golden.py checks this library
+ * against the reference's committed golden vectors (TFastRng64 / std_normal /
+ * FastLogf vectors) and against the upstream CatBoost 1.2.10 end-to-end
+ * fixtures the reference's own oracle tests use (tests/golden/).
+ */
+#ifndef CB_ORACLE_H
+#define CB_ORACLE_H
+
+#include <stdint.h>
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- TFastRng64 (crates/cb-core/src/rng.rs) ---------------------------- */
+typedef struct {
+    uint64_t x1, c1, x2, c2; /* two PCG-XSH-RR LCG streams: state, addend */
+    uint64_t calls;          /* primitive gen_rand draws consumed */
+} orc_rng;
+
+void     orc_rng_new(orc_rng* r, uint64_t seed1, uint32_t seq1, uint64_t seed2, uint32_t seq2);
+void     orc_rng_from_seed(orc_rng* r, uint64_t seed);
+uint64_t orc_rng_gen(orc_rng* r);
+double   orc_rng_real1(orc_rng* r);
+void     orc_rng_advance(orc_rng* r, uint64_t delta);
+uint64_t orc_rng_uniform(orc_rng* r, uint64_t bound);
+double   orc_std_normal(orc_rng* r);
+
+/* ---- FastLogf (crates/cb-train/src/fast_approx.rs) --------------------- */
+float orc_fast_log2f(float v);
+float orc_fast_logf(float v);
+
+/* ---- ordered reduction (crates/cb-core/src/reduction.rs) --------------- */
+double orc_sum_f64(const double* v, int64_t n);
+
+/* ---- quantization (crates/cb-compute/src/histogram.rs:159-165) --------- */
+/* cols: feature-major f32 [F][n]; borders_flat: per-feature ascending f64
+ * borders concatenated, border_counts[f] entries each; out: bins [F][n]. */
+void orc_quantize(const float* cols, int64_t n, int32_t F, const double* borders_flat,
+                  const int32_t* border_counts, uint8_t* out_bins_fm);
+
+/* ---- derivatives (crates/cb-compute/src/loss.rs:35-80) ----------------- */
+enum { ORC_LOSS_RMSE = 0, ORC_LOSS_LOGLOSS = 1, ORC_LOSS_CROSSENTROPY = 2 };
+void orc_compute_gradients(int32_t loss, const double* approx, const double* target, int64_t n,
+                           double* der1, double* der2);
+
+/* ---- bootstrap (crates/cb-train/src/bootstrap.rs) ---------------------- */
+enum { ORC_BOOT_NO = 0, ORC_BOOT_BAYESIAN = 1, ORC_BOOT_BERNOULLI = 2, ORC_BOOT_MVS = 3 };
+int orc_bootstrap(int32_t type, const double* der_obj, int64_t n, double subsample,
+                  float bagging_temperature, int32_t has_prev_leaf_mean, double prev_leaf_mean,
+                  orc_rng* rng, double* out_sample_weights, uint8_t* out_control);
+
+/* ---- one histogram (crates/cb-compute/src/histogram.rs:239-294) -------- */
+/* Sequential object-order f64 scatter: hist[leaf][feature][bin][2] with channel 0
+ * = sum g, channel 1 = sum h.  Objects with leaf >= n_leaves are skipped. */
+void orc_build_histogram(const uint8_t* bins_fm, int64_t n, int32_t F, int32_t n_bins,
+                         const double* g, const double* h, const int32_t* leaf_of,
+                         int32_t n_leaves, double* out_hist);
+
+/* ---- the boosting loop (crates/cb-train/src/boosting.rs CPU branch) ---- */
+enum { ORC_SCORE_COSINE = 0, ORC_SCORE_L2 = 1 };
+
+typedef struct {
+    int64_t n;
+    int32_t n_features;
+    const uint8_t* bins_fm;        /* [F][n] bin indices (bin_of) */
+    const int32_t* border_counts;  /* [F] number of borders per feature */
+    const double* target;          /* [n] */
+    const double* weights;         /* [n] or NULL (unit weights) */
+    int32_t loss;
+    int32_t depth;
+    int32_t iterations;
+    double learning_rate;
+    double l2_leaf_reg;
+    int32_t score_function;
+    int32_t bootstrap_type;
+    double subsample;
+    float bagging_temperature;
+    double random_strength;
+    uint64_t random_seed;
+    int32_t boost_from_average;
+    int32_t n_threads;             /* 0 = OpenMP default */
+} orc_train_args;
+
+typedef struct {
+    int32_t* split_feature;  /* [iterations * depth] (-1 past an early stop) */
+    int32_t* split_bin;      /* [iterations * depth] border index: passes iff bin > split_bin */
+    int32_t* tree_depth;     /* [iterations] splits actually taken */
+    double* leaf_values;     /* [iterations * 2^depth] learning-rate scaled */
+    double* staged;          /* [iterations * n] or NULL */
+    double* final_approx;    /* [n] */
+    double* bias;            /* [1] starting approx */
+    uint64_t* rng_calls;     /* [iterations] main-RNG call count after each tree, or NULL */
+} orc_train_out;
+
+int orc_train(const orc_train_args* a, orc_train_out* o);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,236 @@
+"""ctypes bindings for liboracle.so, the C restatement of catboost_rs's CPU path.
+
+TEST INFRASTRUCTURE ONLY -- the parity checker and the timed CPU baseline.
+Every function mirrors one routine of the reference (file:line given in
+cb_oracle.c); nothing here is used by the product path.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+from dataclasses import dataclass
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "liboracle.so")
+_lib = None
+
+LOSS = {"RMSE": 0, "Logloss": 1, "CrossEntropy": 2}
+BOOT = {"No": 0, "Bayesian": 1, "Bernoulli": 2, "MVS": 3}
+SCORE = {"Cosine": 0, "L2": 1}
+
+
+def build() -> str:
+    """Compile liboracle.so from cb_oracle.c (make, system gcc)."""
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return _LIB_PATH
+
+
+class Rng(C.Structure):
+    _fields_ = [("x1", C.c_uint64), ("c1", C.c_uint64), ("x2", C.c_uint64),
+                ("c2", C.c_uint64), ("calls", C.c_uint64)]
+
+
+class _TrainArgs(C.Structure):
+    _fields_ = [
+        ("n", C.c_int64), ("n_features", C.c_int32),
+        ("bins_fm", C.c_void_p), ("border_counts", C.c_void_p),
+        ("target", C.c_void_p), ("weights", C.c_void_p),
+        ("loss", C.c_int32), ("depth", C.c_int32), ("iterations", C.c_int32),
+        ("learning_rate", C.c_double), ("l2_leaf_reg", C.c_double),
+        ("score_function", C.c_int32), ("bootstrap_type", C.c_int32),
+        ("subsample", C.c_double), ("bagging_temperature", C.c_float),
+        ("random_strength", C.c_double), ("random_seed", C.c_uint64),
+        ("boost_from_average", C.c_int32), ("n_threads", C.c_int32),
+    ]
+
+
+class _TrainOut(C.Structure):
+    _fields_ = [("split_feature", C.c_void_p), ("split_bin", C.c_void_p),
+                ("tree_depth", C.c_void_p), ("leaf_values", C.c_void_p),
+                ("staged", C.c_void_p), ("final_approx", C.c_void_p),
+                ("bias", C.c_void_p), ("rng_calls", C.c_void_p)]
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH):
+            build()
+        L = C.CDLL(_LIB_PATH)
+        P = C.POINTER
+        L.orc_rng_new.argtypes = [P(Rng), C.c_uint64, C.c_uint32, C.c_uint64, C.c_uint32]
+        L.orc_rng_from_seed.argtypes = [P(Rng), C.c_uint64]
+        L.orc_rng_gen.argtypes = [P(Rng)]
+        L.orc_rng_gen.restype = C.c_uint64
+        L.orc_rng_real1.argtypes = [P(Rng)]
+        L.orc_rng_real1.restype = C.c_double
+        L.orc_rng_advance.argtypes = [P(Rng), C.c_uint64]
+        L.orc_rng_uniform.argtypes = [P(Rng), C.c_uint64]
+        L.orc_rng_uniform.restype = C.c_uint64
+        L.orc_std_normal.argtypes = [P(Rng)]
+        L.orc_std_normal.restype = C.c_double
+        L.orc_fast_logf.argtypes = [C.c_float]
+        L.orc_fast_logf.restype = C.c_float
+        L.orc_sum_f64.argtypes = [C.c_void_p, C.c_int64]
+        L.orc_sum_f64.restype = C.c_double
+        L.orc_quantize.argtypes = [C.c_void_p, C.c_int64, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p]
+        L.orc_compute_gradients.argtypes = [C.c_int32, C.c_void_p, C.c_void_p, C.c_int64,
+                                            C.c_void_p, C.c_void_p]
+        L.orc_bootstrap.argtypes = [C.c_int32, C.c_void_p, C.c_int64, C.c_double, C.c_float,
+                                    C.c_int32, C.c_double, P(Rng), C.c_void_p, C.c_void_p]
+        L.orc_bootstrap.restype = C.c_int
+        L.orc_build_histogram.argtypes = [C.c_void_p, C.c_int64, C.c_int32, C.c_int32, C.c_void_p,
+                                          C.c_void_p, C.c_void_p, C.c_int32, C.c_void_p]
+        L.orc_train.argtypes = [P(_TrainArgs), P(_TrainOut)]
+        L.orc_train.restype = C.c_int
+        _lib = L
+    return _lib
+
+
+def _p(a):
+    return None if a is None else a.ctypes.data
+
+
+class TFastRng64:
+    """Host replica of the reference TFastRng64 (crates/cb-core/src/rng.rs)."""
+
+    def __init__(self, seed: int | None = None, *, raw=None):
+        self.s = Rng()
+        if raw is not None:
+            self.s.x1, self.s.c1, self.s.x2, self.s.c2 = raw
+        elif seed is not None:
+            lib().orc_rng_from_seed(C.byref(self.s), C.c_uint64(seed & (2**64 - 1)))
+
+    @classmethod
+    def new(cls, seed1, seq1, seed2, seq2):
+        r = cls()
+        lib().orc_rng_new(C.byref(r.s), seed1, seq1, seed2, seq2)
+        return r
+
+    def gen_rand(self) -> int:
+        return lib().orc_rng_gen(C.byref(self.s))
+
+    def gen_rand_real1(self) -> float:
+        return lib().orc_rng_real1(C.byref(self.s))
+
+    def advance(self, delta: int) -> None:
+        lib().orc_rng_advance(C.byref(self.s), delta)
+
+    def uniform(self, bound: int) -> int:
+        return lib().orc_rng_uniform(C.byref(self.s), bound)
+
+    def std_normal(self) -> float:
+        return lib().orc_std_normal(C.byref(self.s))
+
+    def raw_state(self):
+        return (self.s.x1, self.s.c1, self.s.x2, self.s.c2)
+
+    @property
+    def call_count(self) -> int:
+        return self.s.calls
+
+
+def fast_logf(x: float) -> float:
+    return lib().orc_fast_logf(x)
+
+
+def sum_f64(v) -> float:
+    v = np.ascontiguousarray(v, dtype=np.float64)
+    return lib().orc_sum_f64(_p(v), v.size)
+
+
+def flatten_borders(borders):
+    counts = np.array([len(b) for b in borders], dtype=np.int32)
+    flat = np.ascontiguousarray(np.concatenate([np.asarray(b, dtype=np.float64) for b in borders])
+                                if len(borders) and counts.sum() else np.zeros(0), dtype=np.float64)
+    return flat, counts
+
+
+def quantize(cols_fm: np.ndarray, borders) -> np.ndarray:
+    """bin_of for every (feature, object): cols_fm is f32 [F][n]."""
+    cols = np.ascontiguousarray(cols_fm, dtype=np.float32)
+    F, n = cols.shape
+    flat, counts = flatten_borders(borders)
+    out = np.empty((F, n), dtype=np.uint8)
+    lib().orc_quantize(_p(cols), n, F, _p(flat), _p(counts), _p(out))
+    return out
+
+
+def compute_gradients(loss: str, approx, target):
+    a = np.ascontiguousarray(approx, dtype=np.float64)
+    t = np.ascontiguousarray(target, dtype=np.float64)
+    d1 = np.empty_like(a)
+    d2 = np.empty_like(a)
+    lib().orc_compute_gradients(LOSS[loss], _p(a), _p(t), a.size, _p(d1), _p(d2))
+    return d1, d2
+
+
+def bootstrap(kind: str, der_obj, rng: TFastRng64, subsample=1.0, bagging_temperature=1.0,
+              prev_leaf_mean=None):
+    d = np.ascontiguousarray(der_obj, dtype=np.float64)
+    sw = np.empty_like(d)
+    ctl = np.empty(d.size, dtype=np.uint8)
+    rc = lib().orc_bootstrap(BOOT[kind], _p(d), d.size, subsample, bagging_temperature,
+                             0 if prev_leaf_mean is None else 1,
+                             0.0 if prev_leaf_mean is None else prev_leaf_mean,
+                             C.byref(rng.s), _p(sw), _p(ctl))
+    if rc != 0:
+        raise ValueError(f"bootstrap {kind} failed")
+    return sw, ctl.astype(bool)
+
+
+def build_histogram(bins_fm, g, h, leaf_of=None, n_leaves=1, n_bins=None):
+    bins = np.ascontiguousarray(bins_fm, dtype=np.uint8)
+    F, n = bins.shape
+    nb = int(n_bins if n_bins is not None else (int(bins.max()) + 1 if bins.size else 1))
+    g = np.ascontiguousarray(g, dtype=np.float64)
+    h = np.ascontiguousarray(h, dtype=np.float64)
+    lo = None if leaf_of is None else np.ascontiguousarray(leaf_of, dtype=np.int32)
+    out = np.empty((n_leaves, F, nb, 2), dtype=np.float64)
+    lib().orc_build_histogram(_p(bins), n, F, nb, _p(g), _p(h), _p(lo), n_leaves, _p(out))
+    return out
+
+
+@dataclass
+class OracleFit:
+    split_feature: np.ndarray  # [iters, depth]
+    split_bin: np.ndarray      # [iters, depth]
+    tree_depth: np.ndarray     # [iters]
+    leaf_values: np.ndarray    # [iters, 2^depth] (learning-rate scaled)
+    staged: np.ndarray | None  # [iters, n]
+    final_approx: np.ndarray
+    bias: float
+    rng_calls: np.ndarray
+
+
+def train(bins_fm, border_counts, target, *, loss="RMSE", depth=6, iterations=10,
+          learning_rate=0.1, l2_leaf_reg=3.0, score_function="Cosine", bootstrap_type="No",
+          subsample=0.66, bagging_temperature=1.0, random_strength=0.0, random_seed=0,
+          boost_from_average=True, weights=None, staged=True, n_threads=0) -> OracleFit:
+    """The reference CPU boosting loop (crates/cb-train/src/boosting.rs) on quantized bins."""
+    bins = np.ascontiguousarray(bins_fm, dtype=np.uint8)
+    F, n = bins.shape
+    bc = np.ascontiguousarray(border_counts, dtype=np.int32)
+    t = np.ascontiguousarray(target, dtype=np.float64)
+    w = None if weights is None else np.ascontiguousarray(weights, dtype=np.float64)
+    L = 1 << depth
+    sf = np.empty((iterations, depth), dtype=np.int32)
+    sb = np.empty((iterations, depth), dtype=np.int32)
+    td = np.empty(iterations, dtype=np.int32)
+    lv = np.empty((iterations, L), dtype=np.float64)
+    st = np.empty((iterations, n), dtype=np.float64) if staged else None
+    fa = np.empty(n, dtype=np.float64)
+    bias = np.zeros(1, dtype=np.float64)
+    calls = np.zeros(iterations, dtype=np.uint64)
+    args = _TrainArgs(n, F, _p(bins), _p(bc), _p(t), _p(w), LOSS[loss], depth, iterations,
+                      learning_rate, l2_leaf_reg, SCORE[score_function], BOOT[bootstrap_type],
+                      subsample, bagging_temperature, random_strength, random_seed,
+                      1 if boost_from_average else 0, n_threads)
+    out = _TrainOut(_p(sf), _p(sb), _p(td), _p(lv), _p(st), _p(fa), _p(bias), _p(calls))
+    rc = lib().orc_train(C.byref(args), C.byref(out))
+    if rc != 0:
+        raise RuntimeError(f"orc_train failed rc={rc}")
+    return OracleFit(sf, sb, td, lv, st, fa, float(bias[0]), calls)

@@ -1,0 +1,189 @@
+"""Regenerate the golden fixtures in this directory from the reference checkout.
+
+Run once, in the build container where the reference is mounted:
+
+    python tests/golden/make_golden.py /path/to/catboost_rs
+
+It reads only the reference's committed TEST data -- the golden vectors that
+its unit tests pin (TFastRng64 / std_normal values transcribed from upstream
+fast_ut.cpp, the FastLogf bit-pattern table) and the upstream CatBoost 1.2.10
+end-to-end fixtures its oracle tests train against -- and writes them as small
+.json / .npz files, so the GPU box (which has no reference checkout) can run
+the same parity checks.  No reference source code is copied.
+"""
+from __future__ import annotations
+
+import json
+import os
+import re
+import sys
+
+import numpy as np
+
+OUT = os.path.dirname(os.path.abspath(__file__))
+
+
+def _read(path):
+    with open(path) as f:
+        return f.read()
+
+
+def scalar_vectors(ref):
+    """Known-answer vectors from crates/cb-core/src/{rng,normal}_test.rs."""
+    rng_t = _read(os.path.join(ref, "crates/cb-core/src/rng_test.rs"))
+    first = int(re.search(r"rng\.gen_rand\(\),\s*([0-9_]+)_u64", rng_t).group(1).replace("_", ""))
+    seq = re.search(r"EXPECTED: \[u64; 20\] = \[(.*?)\];", rng_t, re.S).group(1)
+    uniform = [int(x) for x in re.findall(r"\d+", seq)]
+    norm_t = _read(os.path.join(ref, "crates/cb-core/src/normal_test.rs"))
+    vals = re.findall(r"\(n(\w*)\s*-\s*\(?(-?[0-9_.]+e-?\d+)\)?\)\.abs\(\)", norm_t)
+    normals = {}
+    for name, v in vals:
+        normals.setdefault(name, float(v.replace("_", "")))
+    red_t = _read(os.path.join(ref, "crates/cb-core/src/reduction_test.rs"))
+    has_order_lock = "1e16" in red_t
+    fx = os.path.join(ref, "crates/cb-train/tests/fixtures/fast_approx_ref.txt")
+    logf = []
+    for line in _read(fx).splitlines():
+        p = line.split()
+        if len(p) == 3 and p[0] == "fast_logf":
+            logf.append([int(p[1], 16), int(p[2], 16)])
+    return {
+        "source": "crates/cb-core/src/rng_test.rs, normal_test.rs, reduction_test.rs; "
+                  "crates/cb-train/tests/fixtures/fast_approx_ref.txt",
+        "from_seed_17_first_gen_rand": first,
+        "new_0_1_2_3_uniform_100": uniform,
+        "std_normal": {
+            "seed17_first": normals.get("1"),
+            "seed17_second": normals.get("2"),
+            "seed0_first": normals.get("0"),
+            "seed42_first": normals.get("42"),
+            "seed17_draws": [4, 2],
+        },
+        "sum_f64_order_lock": {"values": [1e16, 1.0, -1e16], "expected": 0.0,
+                               "present_in_reference": has_order_lock},
+        "fast_logf_bits": logf,
+    }
+
+
+def _tree_arrays(model, borders):
+    trees = model["oblivious_trees"]
+    depth = max(len(t["splits"]) for t in trees)
+    T = len(trees)
+    sf = np.full((T, depth), -1, dtype=np.int32)
+    sv = np.full((T, depth), np.nan, dtype=np.float64)
+    lv = np.zeros((T, 1 << depth), dtype=np.float64)
+    for i, t in enumerate(trees):
+        for l, s in enumerate(t["splits"]):
+            sf[i, l] = s["float_feature_index"]
+            sv[i, l] = s["border"]
+        v = np.asarray(t["leaf_values"], dtype=np.float64)
+        lv[i, : v.size] = v
+    return sf, sv, lv
+
+
+def _save(name, X, y, borders, params, model, staged=None, weights=None, extra=None):
+    sf, sv, lv = _tree_arrays(model, borders)
+    counts = np.array([len(b) for b in borders], dtype=np.int32)
+    flat = np.concatenate([np.asarray(b, dtype=np.float64) for b in borders]) if counts.sum() else np.zeros(0)
+    arrays = dict(X=np.asarray(X, dtype=np.float32), y=np.asarray(y, dtype=np.float64),
+                  borders_flat=flat, border_counts=counts, split_feature=sf, split_border=sv,
+                  leaf_values=lv, params=np.array(json.dumps(params)))
+    if staged is not None:
+        arrays["staged"] = np.asarray(staged, dtype=np.float64).reshape(lv.shape[0], -1)
+    if weights is not None:
+        arrays["weights"] = np.asarray(weights, dtype=np.float64)
+    for k, v in (extra or {}).items():
+        arrays[k] = v
+    np.savez_compressed(os.path.join(OUT, f"e2e_{name}.npz"), **arrays)
+
+
+def _params(cfg_params, loss):
+    p = cfg_params
+    return {
+        "loss": loss,
+        "depth": int(p["depth"]),
+        "iterations": int(p["iterations"]),
+        "learning_rate": float(p["learning_rate"]),
+        "l2_leaf_reg": float(p["l2_leaf_reg"]),
+        "score_function": p.get("score_function", "Cosine"),
+        "bootstrap_type": p.get("bootstrap_type", "No").replace("MVS", "MVS"),
+        "subsample": float(p.get("subsample", 0.66 if p.get("bootstrap_type") == "Bernoulli" else 0.8)),
+        "bagging_temperature": float(p.get("bagging_temperature", 1.0)),
+        "random_strength": float(p.get("random_strength", 0.0)),
+        "random_seed": int(p.get("random_seed", 0)),
+        "boost_from_average": bool(p.get("boost_from_average", False)),
+    }
+
+
+def e2e_fixtures(ref):
+    fx = os.path.join(ref, "crates/cb-oracle/fixtures")
+    ld = lambda *p: np.load(os.path.join(fx, *p))  # noqa: E731
+    jl = lambda *p: json.loads(_read(os.path.join(fx, *p)))  # noqa: E731
+    written = []
+
+    def borders_of(model):
+        return [f["borders"] for f in model["features_info"]["float_features"]]
+
+    # numeric_tiny skeletons (crates/cb-train/tests/slice_first_oracle_test.rs)
+    Xt, yt = ld("inputs/numeric_tiny/X.npy"), ld("inputs/numeric_tiny/y.npy")
+    for scen, loss in (("regression_skeleton", "RMSE"), ("binclf_skeleton", "Logloss")):
+        cfg, model = jl(scen, "config.json"), jl(scen, "model.json")
+        y = yt if loss == "RMSE" else (yt > np.median(yt)).astype(np.float64)
+        _save(scen, Xt, y, borders_of(model), _params(cfg["params"], loss), model, ld(scen, "staged.npy"))
+        written.append(scen)
+    # regularization family on numeric_tiny
+    for sub in ("l2", "bagging_temp", "random_strength", "random_strength_bernoulli"):
+        scen = f"regularization/{sub}"
+        cfg, model = jl(scen, "config.json"), jl(scen, "model.json")
+        _save(scen.replace("/", "_"), Xt, yt, borders_of(model), _params(cfg["params"], "RMSE"), model,
+              ld(scen, "staged.npy"))
+        written.append(scen)
+    # bootstrap families on the 1500-row multi-block input
+    Xb, yb = ld("inputs/bootstrap_multiblock/X.npy"), ld("inputs/bootstrap_multiblock/y.npy")
+    scen_list = [f"bootstrap/{k}" for k in ("no", "bayesian", "bernoulli", "mvs")]
+    scen_list += [f"bootstrap_dev/{k}" for k in ("no", "bayesian", "bernoulli", "mvs")]
+    scen_list += [f"mvs_seeds/s{s}_bfa{b}" for s in range(5) for b in (0, 1)]
+    for scen in scen_list:
+        cfg, model = jl(scen, "config.json"), jl(scen, "model.json")
+        _save(scen.replace("/", "_"), Xb, yb, borders_of(model), _params(cfg["params"], "RMSE"), model,
+              ld(scen, "staged.npy"))
+        written.append(scen)
+    # weighted / biased device-parity fixtures with their FULL border sets
+    for scen in ("weighted_device_sym", "bias_device_sym"):
+        cfg, model = jl(scen, "config.json"), jl(scen, "model.json")
+        B = ld(scen, "borders.npy")
+        w = ld(scen, "weights.npy") if os.path.exists(os.path.join(fx, scen, "weights.npy")) else None
+        Xs = ld(scen, "X.npy")
+        preds = ld(scen, "predictions.npy")
+        _save(scen, Xs, ld(scen, "y.npy"), [list(r) for r in B], _params(cfg["params"], "RMSE"), model,
+              weights=w, extra={"predictions": preds})
+        written.append(scen)
+    # NaN handling, both sentinel modes (model borders carry the sentinel)
+    cfg = jl("nan_mode", "config.json")
+    for mode in ("Min", "Max"):
+        model = jl("nan_mode", f"model_{mode}.json")
+        _save(f"nan_mode_{mode}", ld("nan_mode", "X.npy"), ld("nan_mode", "y.npy"), borders_of(model),
+              _params(cfg["params"], "RMSE"), model,
+              extra={"X_eval": ld("nan_mode", "X_eval.npy").astype(np.float32),
+                     "preds_eval": ld("nan_mode", f"preds_{mode}.npy")})
+        written.append(f"nan_mode/{mode}")
+    return written
+
+
+def main():
+    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("CB_REFERENCE", "")
+    if not ref or not os.path.isdir(ref):
+        sys.exit("usage: make_golden.py <reference checkout>")
+    with open(os.path.join(OUT, "scalar_vectors.json"), "w") as f:
+        json.dump(scalar_vectors(ref), f, indent=1)
+    written = e2e_fixtures(ref)
+    with open(os.path.join(OUT, "MANIFEST.json"), "w") as f:
+        json.dump({"generator": "tests/golden/make_golden.py",
+                   "origin": "upstream CatBoost 1.2.10 fixtures committed under the reference's "
+                             "crates/cb-oracle/fixtures (thread_count=1, random_strength per scenario)",
+                   "scenarios": written}, f, indent=1)
+    print("wrote", len(written), "scenarios")
+
+
+if __name__ == "__main__":
+    main()
