@@ -1,0 +1,385 @@
+#!/usr/bin/env python
+"""Benchmark: trees/sec on BASELINE config 2 (Logloss, 10M x 200 float32 features,
+half N(0,1) / half U(0,1), 5% NaN, border_count 128 (nan_mode=Min sentinel),
+depth 8, lr 0.05, Bayesian bootstrap T=1, Cosine score, l2 3), plus the
+histogram kernel's achieved HBM bandwidth against the measured peak.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+A step is one boosting iteration (one tree).  Multi-GPU runs are launched by
+torchrun, one rank per GPU; rows are document-sharded (strong scaling: the
+10M-row job is split across the ranks) and every level's histograms are summed
+with NCCL.  Rank 0 prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+BLOCK_ROWS = 1 << 20       # data is generated in fixed 1Mi-row blocks so any sharding sees the same rows
+BORDER_SAMPLE = 200_000    # fixed-seed sample the borders are selected from (cf. cb-data's 200k sample)
+FMIN = float(np.finfo(np.float32).min)
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# synthetic data (config 2 shapes and distributions; no public dataset exists)
+# ---------------------------------------------------------------------------
+
+def _block(b: int, F: int, seed: int):
+    """Rows [b*BLOCK_ROWS, (b+1)*BLOCK_ROWS): features [F][rows] f32 and label."""
+    g = np.random.default_rng([seed, b])
+    m = BLOCK_ROWS
+    X = np.empty((F, m), dtype=np.float32)
+    h = F // 2
+    X[:h] = g.standard_normal((h, m), dtype=np.float32)
+    X[h:] = g.random((F - h, m), dtype=np.float32)
+    nan = g.random((F, m), dtype=np.float32) < 0.05
+    X[nan] = np.nan
+    # label ~ Bernoulli(sigmoid(sparse linear over 20 features + pairwise terms))
+    gw = np.random.default_rng([seed, 1 << 30])
+    feats = gw.choice(F, size=20, replace=False)
+    coef = gw.standard_normal(20)
+    pairs = gw.choice(20, size=(10, 2))
+    pcoef = gw.standard_normal(10) * 0.5
+    Z = np.nan_to_num(X[feats].astype(np.float64))
+    z = coef @ Z
+    for (i, j), c in zip(pairs, pcoef):
+        z += c * Z[i] * Z[j]
+    y = (g.random(m) < 1.0 / (1.0 + np.exp(-z))).astype(np.float64)
+    return X, y
+
+
+def make_shard(row_offset: int, n: int, F: int, seed: int):
+    X = np.empty((F, n), dtype=np.float32)
+    y = np.empty(n, dtype=np.float64)
+    b0, b1 = row_offset // BLOCK_ROWS, (row_offset + n - 1) // BLOCK_ROWS
+    for b in range(b0, b1 + 1):
+        Xb, yb = _block(b, F, seed)
+        lo = max(row_offset, b * BLOCK_ROWS)
+        hi = min(row_offset + n, (b + 1) * BLOCK_ROWS)
+        X[:, lo - row_offset:hi - row_offset] = Xb[:, lo - b * BLOCK_ROWS:hi - b * BLOCK_ROWS]
+        y[lo - row_offset:hi - row_offset] = yb[lo - b * BLOCK_ROWS:hi - b * BLOCK_ROWS]
+    return X, y
+
+
+def make_borders(F: int, border_count: int, seed: int):
+    """Uniform-quantile borders from a fixed-seed sample of the same distribution;
+    NaN-bearing columns get the nan_mode=Min sentinel (border_count includes it)."""
+    g = np.random.default_rng([seed, 1 << 31])
+    h = F // 2
+    S = np.empty((F, BORDER_SAMPLE), dtype=np.float32)
+    S[:h] = g.standard_normal((h, BORDER_SAMPLE), dtype=np.float32)
+    S[h:] = g.random((F - h, BORDER_SAMPLE), dtype=np.float32)
+    out = []
+    k = border_count - 1
+    for f in range(F):
+        q = np.quantile(S[f].astype(np.float64), np.linspace(0, 1, k + 2)[1:-1])
+        b = np.unique(q.astype(np.float32).astype(np.float64))
+        out.append(np.concatenate([[FMIN], b]))
+    return out
+
+
+def shard_bounds(n_total: int, world: int, rank: int):
+    per = -(-n_total // world)
+    per = -(-per // 8192) * 8192  # MVS-aligned shards
+    lo = min(n_total, rank * per)
+    hi = min(n_total, lo + per)
+    return lo, hi - lo
+
+
+# ---------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.rows = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([x.strip() for x in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        sm = [float(r[1]) for r in self.rows if len(r) > 2 and r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if len(r) > 2 and r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for r in self.rows:
+            for k, nm in enumerate(names):
+                if len(r) > 5 + k and r[5 + k].lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(self.rows)}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline / reference arm: the C restatement of the reference CPU path
+# ---------------------------------------------------------------------------
+
+def cpu_reference_run(args, n_sample: int, trees: int, warm: int):
+    from oracle import oracle as orc
+    F = args.features
+    X, y = make_shard(0, n_sample, F, args.seed)
+    borders = make_borders(F, args.border_count, args.seed)
+    bins = orc.quantize(X, borders)
+    del X
+    threads = os.cpu_count() or 1
+    kw = dict(loss="Logloss", depth=args.depth, learning_rate=0.05, l2_leaf_reg=3.0,
+              score_function="Cosine", bootstrap_type="Bayesian", bagging_temperature=1.0,
+              random_seed=0, boost_from_average=False, staged=False, n_threads=threads)
+    if warm:
+        orc.train(bins, [len(b) for b in borders], y, iterations=warm, **kw)
+    t0 = time.perf_counter()
+    orc.train(bins, [len(b) for b in borders], y, iterations=trees, **kw)
+    dt = time.perf_counter() - t0
+    per_tree_sample = dt / trees
+    # CPU cost per tree is linear in rows (every level visits every row per feature)
+    per_tree_full = per_tree_sample * (args.rows / n_sample)
+    return 1.0 / per_tree_full, threads, dt
+
+
+# ---------------------------------------------------------------------------
+# main
+# ---------------------------------------------------------------------------
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--rows", type=int, default=10_000_000)
+    ap.add_argument("--features", type=int, default=200)
+    ap.add_argument("--depth", type=int, default=8)
+    ap.add_argument("--border-count", type=int, default=128)
+    ap.add_argument("--seed", type=int, default=20261201)
+    ap.add_argument("--cpu-sample-rows", type=int, default=500_000)
+    ap.add_argument("--cpu-trees", type=int, default=2)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    metric = "trees/sec at 10M x 200 depth-8 Logloss"
+    base_cfg = {"workload": "config2: Logloss 10M x 200 f32 (half N(0,1), half U(0,1), 5% NaN), "
+                            "border_count 128 (nan_mode Min), depth 8, lr 0.05, Bayesian T=1, Cosine, l2 3",
+                "rows": args.rows, "features": args.features, "depth": args.depth,
+                "border_count": args.border_count, "parallelism": f"doc-shard x{world}",
+                "l2_flush": "inputs larger than L2 (2.2 GB of row-major bins re-read per tree)"}
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        per = (args.steps + args.warmup)
+        # bounded sample: about a minute of CPU work for the whole run
+        sample = min(args.rows, args.cpu_sample_rows)
+        tps, cores, dt = cpu_reference_run(args, sample, args.steps, args.warmup)
+        line = {"impl": "reference", "metric": metric, "value": tps, "unit": "trees/s",
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": 1e3 / tps, "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "f64", "data": "synthetic", "config": base_cfg,
+                "cpu_baseline": {"value": tps, "unit": "trees/s", "cores": cores, "kind": "port",
+                                 "sample": f"C restatement of the reference CPU path (oracle/), {sample} rows x "
+                                           f"{args.features} features, {args.steps} timed trees after "
+                                           f"{args.warmup} warm-up; time per tree scaled by {args.rows}/{sample} "
+                                           f"(per-tree CPU cost is linear in rows)"},
+                "e2e": {"value": tps, "unit": "trees/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+
+    import torch
+    import catboost_rs_b200 as cb
+
+    torch.cuda.set_device(local_rank)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+
+    F = args.features
+    row_offset, n = shard_bounds(args.rows, world, rank)
+    X, y = make_shard(row_offset, n, F, args.seed)
+    borders = make_borders(F, args.border_count, args.seed)
+    cols = [X[f] for f in range(F)]
+    uid = None
+    if world > 1:
+        obj = [cb.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        uid = obj[0]
+
+    def open_session(sample_from_host: bool):
+        rt = cb.B200Runtime()
+        cfg = cb.DeviceTrainConfig(bootstrap_type="Bayesian", bagging_temperature=1.0, rng_seed=0, bias=0.0,
+                                   sample_from_host=sample_from_host, device=local_rank, rank=rank,
+                                   world_size=world, row_offset=row_offset, n_total=args.rows,
+                                   nccl_unique_id=uid)
+        ok = rt.begin_device_training_raw("Logloss", args.depth, True, 1, "Cosine", cols, borders, None, n, F,
+                                          max(len(b) for b in borders) + 1, 0.05, 3.0, cfg)
+        if not ok:
+            raise RuntimeError(rt.decline_reason)
+        return rt
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # ---- device-resident throughput (value) -------------------------------
+    rt = open_session(False)
+    rt.set_profiling(True)  # per-kernel CUDA events; read after each tree's final sync
+    for _ in range(args.warmup):
+        rt.grow_tree_on_device(None, y, [], leaf_of_bytes=0, resident_approx=True)
+    hist_ms = rows = launches = 0.0
+    stage = np.zeros(8)
+    barrier()
+    with ClockSampler(local_rank) as clk:
+        rt.mark(0)
+        for _ in range(args.steps):
+            rt.grow_tree_on_device(None, y, [], leaf_of_bytes=0, resident_approx=True)
+            tm = rt.timing()
+            stage += tm
+            hist_ms += tm[1]
+            rows += tm[6]
+            launches += tm[7]
+        rt.mark(1)
+        elapsed = rt.elapsed_ms(0, 1)
+        barrier()
+    elapsed = max_over_ranks(elapsed)
+    rt.end_device_training()
+    value = args.steps / (elapsed / 1e3)
+
+    # histogram roofline: algorithmic bytes = rows x (F bins + 16 B g/h) + 4 B index per gathered row
+    lvl0_rows = args.steps * n
+    alg_bytes = rows * (F + 16) + (rows - lvl0_rows) * 4
+    hist_launches = args.steps * args.depth
+    achieved = alg_bytes / (hist_ms / 1e3) / 1e9 if hist_ms > 0 else None
+    peak, peak_kind = peaks()
+
+    # ---- end to end through the C ABI with host buffers (e2e) --------------
+    e2e = None
+    if not args.no_e2e:
+        rt2 = open_session(True)
+        pin = lambda shape, dt: torch.empty(shape, dtype=dt, pin_memory=True).numpy()  # noqa: E731
+        sample = pin((n,), torch.float64)
+        rs = np.random.default_rng(7)
+        sample[:] = -np.log(rs.random(n))  # Bayesian-like multipliers; content does not change the cost
+        leaf_of = pin((n,), torch.uint8)
+        import ctypes as C
+        L = cb.load_library()
+        D = args.depth
+        sf = np.empty(D, np.int32)
+        sb = np.empty(D, np.int32)
+        ns = np.zeros(1, np.int32)
+        lv = np.empty(1 << D, np.float64)
+        yy = np.ascontiguousarray(y)
+
+        def step():
+            rc = L.cbgpu_grow_tree(rt2._s, None, yy.ctypes.data, n, sample.ctypes.data, n, sf.ctypes.data,
+                                   sb.ctypes.data, ns.ctypes.data, lv.ctypes.data, leaf_of.ctypes.data, 1)
+            if rc:
+                raise RuntimeError(cb._lib.last_error())
+        for _ in range(args.warmup):
+            step()
+        barrier()
+        rt2.mark(0)
+        for _ in range(args.steps):
+            step()
+        rt2.mark(1)
+        e_ms = max_over_ranks(rt2.elapsed_ms(0, 1))
+        barrier()
+        rt2.end_device_training()
+        e2e = {"value": args.steps / (e_ms / 1e3), "unit": "trees/s", "h2d_bytes_per_step": int(n * 8),
+               "d2h_bytes_per_step": int(n + D * 8 + (1 << D) * 8),
+               "path": "cbgpu_grow_tree with a pinned host bootstrap sample (sample_from_host, the cb-train "
+                       "contract) uploaded and u8 leaf ids read back every tree"}
+
+    # ---- CPU baseline (rank 0, N=1 only) -------------------------------------
+    cpu = None
+    if world == 1 and not args.no_cpu:
+        sample = min(args.rows, args.cpu_sample_rows)
+        tps, cores, dt = cpu_reference_run(args, sample, args.cpu_trees, 0)
+        cpu = {"value": tps, "unit": "trees/s", "cores": cores, "kind": "port",
+               "sample": f"C restatement of the reference CPU path (oracle/) on {sample} rows x {F} features, "
+                         f"{args.cpu_trees} trees ({dt:.1f} s), time per tree scaled by {args.rows}/{sample}"}
+
+    if rank == 0:
+        line = {"metric": metric, "value": value, "unit": "trees/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": elapsed / args.steps, "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "int64",
+                "data": "synthetic (seeded, config-2 shapes and distributions)", "config": base_cfg,
+                "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                             "frac": (achieved / peak) if achieved else None, "traffic": None,
+                             "kernel": "hist_kernel", "peak_kind": peak_kind,
+                             "algorithmic_bytes_per_launch": alg_bytes / hist_launches,
+                             "avg_launch_ms": hist_ms / hist_launches},
+                "stage_ms_per_tree": {k: float(stage[i] / args.steps) for i, k in
+                                      enumerate(["tree", "hist", "derive_score", "partition", "der_bootstrap",
+                                                 "collectives"])},
+                "hist_rows_per_tree": rows / args.steps,
+                "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches), "clocks": clk.summary()}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,13 @@
+"""catboost_rs_b200 -- B200-native oblivious-tree training path for catboost_rs.
+
+The compute is libcbgpu.so (CUDA for sm_100a behind the C ABI in
+include/cbgpu.h).  This package holds the host-side mirror of the reference's
+`cb_compute::Runtime` seam (runtime.py), the boosting loop that drives it
+(boosting.py) and the build script (build.py).
+"""
+from ._lib import CbGpuError, load as load_library  # noqa: F401
+from .runtime import (B200Runtime, DeviceGrownTree, DeviceTrainConfig, Derivatives,  # noqa: F401
+                      bootstrap_weights, histogram, nccl_unique_id)
+from .boosting import FitParams, ObliviousModel, fit, seq_sum, starting_approx  # noqa: F401
+
+__version__ = "0.1.0"

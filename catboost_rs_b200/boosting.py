@@ -1,0 +1,135 @@
+"""The boosting loop on top of the B200 runtime, mirroring cb-train's device
+branch (crates/cb-train/src/boosting.rs:6532-7300) for the covered regime:
+SymmetricTree, RMSE / Logloss / CrossEntropy, Plain, Cosine / L2, Gradient
+leaves, bootstrap No / Bayesian / Bernoulli / MVS.
+
+The session keeps the approximant and the bootstrap resident on the device and
+replays the main RNG stream's draw accounting itself (PRE draws, bootstrap,
+per-level replay, POST draws), so trees match the CPU path.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import Optional, Sequence
+
+import numpy as np
+
+from .runtime import B200Runtime, DeviceTrainConfig
+
+
+@dataclass
+class FitParams:
+    loss: str = "RMSE"
+    depth: int = 6
+    iterations: int = 100
+    learning_rate: float = 0.1
+    l2_leaf_reg: float = 3.0
+    score_function: str = "Cosine"
+    bootstrap_type: str = "No"
+    subsample: float = 0.8
+    bagging_temperature: float = 1.0
+    random_seed: int = 0
+    boost_from_average: bool = True
+
+
+@dataclass
+class ObliviousModel:
+    """Per-tree splits (feature, border index; level l is leaf bit l), the
+    learning-rate scaled leaf values, the borders and the bias."""
+    borders: list
+    split_feature: np.ndarray
+    split_bin: np.ndarray
+    leaf_values: np.ndarray
+    bias: float
+    staged: Optional[np.ndarray] = None
+    stage_timing: list = field(default_factory=list)
+
+    def split_borders(self) -> np.ndarray:
+        return np.array([[self.borders[f][b] for f, b in zip(rf, rb)]
+                         for rf, rb in zip(self.split_feature, self.split_bin)])
+
+    def predict(self, X) -> np.ndarray:
+        """Raw approximant for rows of X (f32 [n, F]); float value > border passes,
+        NaN passes only on nan_mode=Max features (border list ends with f32::MAX)."""
+        X = np.asarray(X, dtype=np.float32)
+        out = np.full(X.shape[0], self.bias, dtype=np.float64)
+        fmax = np.float64(np.finfo(np.float32).max)
+        for t in range(self.split_feature.shape[0]):
+            leaf = np.zeros(X.shape[0], dtype=np.int64)
+            for l in range(self.split_feature.shape[1]):
+                f = int(self.split_feature[t, l])
+                b = self.borders[f][int(self.split_bin[t, l])]
+                v = X[:, f].astype(np.float64)
+                nan_max = len(self.borders[f]) > 0 and self.borders[f][-1] == fmax
+                leaf |= (((v > b) | (np.isnan(v) & nan_max)).astype(np.int64)) << l
+            out += self.leaf_values[t][leaf]
+        return out
+
+
+def seq_sum(v) -> float:
+    """Strict left-to-right f64 sum (cb_core::sum_f64): numpy's cumsum is sequential."""
+    v = np.asarray(v, dtype=np.float64)
+    return float(np.cumsum(v)[-1]) if v.size else 0.0
+
+
+def starting_approx(p: FitParams, target) -> float:
+    """boosting.rs:1871: mean target for RMSE with boost_from_average, else 0."""
+    if p.boost_from_average and p.loss == "RMSE" and len(target):
+        return seq_sum(target) / len(target)
+    return 0.0
+
+
+def fit(float_columns: Sequence[np.ndarray], borders: Sequence[Sequence[float]], target,
+        params: FitParams, weights=None, *, staged: bool = False, device: int = 0,
+        placement: Optional[dict] = None, profile: bool = False,
+        bias: Optional[float] = None, sum_weights: Optional[float] = None) -> ObliviousModel:
+    """Fit on raw f32 columns with fixed borders (device quantization).
+
+    `placement` = {rank, world_size, row_offset, n_total, nccl_unique_id} for a
+    document-sharded fit (one process per GPU); `bias` / `sum_weights` are then
+    the GLOBAL starting approximant and weight total.
+    """
+    p = params
+    cols = [np.ascontiguousarray(c, dtype=np.float32) for c in float_columns]
+    F = len(cols)
+    n = cols[0].size if F else 0
+    t = np.ascontiguousarray(target, dtype=np.float64)
+    w = None if weights is None else np.ascontiguousarray(weights, dtype=np.float64)
+    pl = placement or {}
+    n_total = pl.get("n_total", n)
+    sw = sum_weights if sum_weights is not None else (seq_sum(w) if w is not None else float(n))
+    scaled_l2 = p.l2_leaf_reg * (sw / n_total) if n_total else p.l2_leaf_reg
+    b0 = bias if bias is not None else starting_approx(p, t)
+    n_bins = max(len(b) for b in borders) + 1
+    cfg = DeviceTrainConfig(bootstrap_type=p.bootstrap_type, sample_rate=p.subsample,
+                            rng_seed=p.random_seed, bias=b0, sample_from_host=False,
+                            bagging_temperature=p.bagging_temperature, device=device,
+                            rank=pl.get("rank", 0), world_size=pl.get("world_size", 1),
+                            row_offset=pl.get("row_offset", 0), n_total=n_total,
+                            nccl_unique_id=pl.get("nccl_unique_id"))
+    rt = B200Runtime()
+    ok = rt.begin_device_training_raw(p.loss, p.depth, True, 1, p.score_function, cols, borders, w,
+                                      n, F, n_bins, p.learning_rate, scaled_l2, cfg)
+    if not ok:
+        raise RuntimeError(f"device declined: {rt.decline_reason}")
+    if profile:
+        rt.set_profiling(True)
+    T, D = p.iterations, p.depth
+    sf = np.zeros((T, D), dtype=np.int32)
+    sb = np.zeros((T, D), dtype=np.int32)
+    lv = np.zeros((T, 1 << D), dtype=np.float64)
+    st = np.zeros((T, n), dtype=np.float64) if staged else None
+    timings = []
+    try:
+        for it in range(T):
+            tree = rt.grow_tree_on_device(None, t, [], leaf_of_bytes=0, resident_approx=True)
+            for l, (f, b, _) in enumerate(tree.splits):
+                sf[it, l], sb[it, l] = f, b
+            lv[it] = tree.leaf_values * p.learning_rate  # normalize_leaf_values
+            if staged:
+                st[it] = rt.resident_approx()
+            if profile:
+                timings.append(rt.timing().copy())
+    finally:
+        rt.end_device_training()
+    return ObliviousModel([np.asarray(b, dtype=np.float64) for b in borders], sf, sb, lv, b0, st, timings)

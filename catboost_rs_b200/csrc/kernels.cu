@@ -1,0 +1,1195 @@
+// kernels.cu -- sm_100a kernels of the oblivious-tree training path.
+//
+// Per tree: bootstrap -> fused apply/derivative -> fixed-point scales, then per
+// level: histogram (smaller children only) -> derive siblings + bin prefix ->
+// score + argmax -> stable partition of the leaf-sorted row order; the last
+// level routes and reduces the leaf sums.  Every reduction whose result feeds a
+// split decision is an exact int64 fixed-point sum, so results do not depend on
+// launch geometry, atomic order or the number of GPUs.
+//
+// Compiled with -fmad=false: every f64 expression rounds each operation as the
+// reference's Rust code does (no FMA contraction).
+#include <cfloat>
+#include <cstdio>
+
+#include "kernels.cuh"
+
+namespace cbgpu {
+
+namespace {
+
+constexpr unsigned kFull = 0xffffffffu;
+
+template <typename T>
+__device__ __forceinline__ T warp_incl_scan(T v) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        T y = __shfl_up_sync(kFull, v, o);
+        if (lane >= o) v += y;
+    }
+    return v;
+}
+
+// Exclusive block scan (blockDim multiple of 32, <= 1024).  `sm` holds >= 33 T.
+template <typename T>
+__device__ __forceinline__ T block_excl_scan(T v, T* sm, T* total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    T inc = warp_incl_scan(v);
+    if (lane == 31) sm[warp] = inc;
+    __syncthreads();
+    if (warp == 0) {
+        T s = lane < nw ? sm[lane] : T(0);
+        s = warp_incl_scan(s);
+        sm[lane] = s;
+    }
+    __syncthreads();
+    T off = warp ? sm[warp - 1] : T(0);
+    if (total) *total = sm[nw - 1];
+    __syncthreads();
+    return off + inc - v;
+}
+
+__device__ __forceinline__ double nan_to_neg_inf(double s) { return s == s ? s : -INFINITY; }
+
+// (score, index) better than (bs, bi)?  Strict > with lowest index on ties,
+// which is the CPU's first-wins strict-> scan order (tree.rs:355-366).
+__device__ __forceinline__ bool better(double s, int i, double bs, int bi) {
+    return s > bs || (s == bs && i < bi);
+}
+
+}  // namespace
+
+// ============================================================================
+// begin: quantization and layout
+// ============================================================================
+
+// bin = #{k : borders[k] < value} over ascending borders (histogram.rs:159-165);
+// NaN -> 0, or the top bin when the last border is the f32::MAX sentinel.
+__global__ void quantize_column_kernel(const float* __restrict__ col, int64_t n,
+                                       const double* __restrict__ borders, int32_t nb,
+                                       uint8_t* __restrict__ out, uint32_t* err) {
+    __shared__ double sb[256];
+    for (int k = threadIdx.x; k < nb; k += blockDim.x) sb[k] = borders[k];
+    __syncthreads();
+    const bool nan_top = nb > 0 && sb[nb - 1] == (double)FLT_MAX;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        float v = col[i];
+        uint32_t b;
+        if (v != v) {
+            b = nan_top ? (uint32_t)nb : 0u;
+        } else {
+            double x = (double)v;
+            int lo = 0, hi = nb;
+            while (lo < hi) {
+                int mid = (lo + hi) >> 1;
+                if (sb[mid] < x) lo = mid + 1; else hi = mid;
+            }
+            b = (uint32_t)lo;
+        }
+        out[i] = (uint8_t)b;
+    }
+    (void)err;
+}
+
+void launch_quantize_column(const float* col, int64_t n, const double* borders, int32_t nb,
+                            uint8_t* out, uint32_t* err, cudaStream_t st) {
+    int64_t blocks = (n + 1023) / 1024;
+    if (blocks > 4096) blocks = 4096;
+    if (blocks < 1) blocks = 1;
+    quantize_column_kernel<<<(unsigned)blocks, 256, 0, st>>>(col, n, borders, nb, out, err);
+}
+
+__global__ void u32_to_u8_kernel(const uint32_t* __restrict__ col, int64_t n, int32_t n_bins,
+                                 uint8_t* __restrict__ out, uint32_t* err) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        uint32_t b = col[i];
+        if (b >= (uint32_t)n_bins) {
+            atomicOr(err, kErrBinRange);
+            b = 0;
+        }
+        out[i] = (uint8_t)b;
+    }
+}
+
+void launch_u32_to_u8_column(const uint32_t* col, int64_t n, int32_t n_bins, uint8_t* out,
+                             uint32_t* err, cudaStream_t st) {
+    int64_t blocks = (n + 1023) / 1024;
+    if (blocks > 4096) blocks = 4096;
+    if (blocks < 1) blocks = 1;
+    u32_to_u8_kernel<<<(unsigned)blocks, 256, 0, st>>>(col, n, n_bins, out, err);
+}
+
+// Feature-major [F][n_stride] -> row-major [n][F_pad] via a 32-feature x 128-row
+// shared tile; padding features are written as 0.
+__global__ void transpose_fm_rm_kernel(const uint8_t* __restrict__ fm, int64_t n, int64_t n_stride,
+                                       int32_t F, uint8_t* __restrict__ rm, int32_t F_pad) {
+    __shared__ uint8_t tile[32][128 + 4];
+    const int64_t r0 = (int64_t)blockIdx.x * 128;
+    const int f0 = blockIdx.y * 32;
+    for (int k = threadIdx.x; k < 32 * 128; k += blockDim.x) {
+        int fl = k / 128, rl = k % 128;
+        int64_t r = r0 + rl;
+        int f = f0 + fl;
+        tile[fl][rl] = (f < F && r < n) ? fm[(int64_t)f * n_stride + r] : (uint8_t)0;
+    }
+    __syncthreads();
+    for (int k = threadIdx.x; k < 32 * 128; k += blockDim.x) {
+        int rl = k / 32, fl = k % 32;
+        int64_t r = r0 + rl;
+        if (r < n) rm[r * F_pad + f0 + fl] = tile[fl][rl];
+    }
+}
+
+void launch_transpose_fm_to_rm(const uint8_t* fm, int64_t n, int64_t n_stride, int32_t F,
+                               uint8_t* rm, int32_t F_pad, cudaStream_t st) {
+    dim3 grid((unsigned)((n + 127) / 128), (unsigned)(F_pad / 32));
+    if (grid.x == 0) return;
+    transpose_fm_rm_kernel<<<grid, 256, 0, st>>>(fm, n, n_stride, F, rm, F_pad);
+}
+
+__global__ void transpose_rm_fm_kernel(const uint8_t* __restrict__ rm, int64_t n, int32_t F,
+                                       int32_t F_src, uint8_t* __restrict__ fm, int64_t n_stride) {
+    for (int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < n * F;
+         k += (int64_t)gridDim.x * blockDim.x) {
+        int64_t r = k / F;
+        int f = (int)(k % F);
+        fm[(int64_t)f * n_stride + r] = rm[r * F_src + f];
+    }
+}
+
+void launch_transpose_rm_to_fm(const uint8_t* rm, int64_t n, int32_t F, int32_t F_src,
+                               uint8_t* fm, int64_t n_stride, cudaStream_t st) {
+    int64_t blocks = (n * F + 1023) / 1024;
+    if (blocks > 8192) blocks = 8192;
+    if (blocks < 1) blocks = 1;
+    transpose_rm_fm_kernel<<<(unsigned)blocks, 256, 0, st>>>(rm, n, F, F_src, fm, n_stride);
+}
+
+// ============================================================================
+// bootstrap (crates/cb-train/src/bootstrap.rs)
+// ============================================================================
+
+// Bayesian: 1000-row blocks, block b draws from from_seed(rand_seed + b)
+// advanced 10 then one gen_rand_real1 per row (bootstrap.rs:152-175).
+// Bernoulli: the main stream continues across rows: row g uses the base state
+// advanced g draws (set_sampled_control, bootstrap.rs:178-184).  Each thread
+// jumps once and steps kBootRun consecutive rows.
+__global__ void bootstrap_kernel(int mode, int64_t n, int64_t row_offset, uint64_t rand_seed,
+                                 Rng64 base, double rate, float temp, float* __restrict__ out) {
+    int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    int64_t i0 = t * kBootRun;
+    if (i0 >= n) return;
+    int64_t g0 = row_offset + i0;
+    if (mode == 1) {
+        Rng64 r = Rng64::from_seed(rand_seed + (uint64_t)(g0 / 1000));
+        r.advance(10 + (uint64_t)(g0 % 1000));
+        for (int j = 0; j < kBootRun && i0 + j < n; ++j) {
+            int64_t g = g0 + j;
+            if (j > 0 && g % 1000 == 0) {
+                r = Rng64::from_seed(rand_seed + (uint64_t)(g / 1000));
+                r.advance(10);
+            }
+            out[i0 + j] = (float)bayesian_weight(real1(r), temp);
+        }
+    } else {
+        Rng64 r = base;
+        r.advance((uint64_t)g0);
+        for (int j = 0; j < kBootRun && i0 + j < n; ++j) out[i0 + j] = real1(r) < rate ? 1.0f : 0.0f;
+    }
+}
+
+void launch_bootstrap(int mode, int64_t n, int64_t row_offset, uint64_t rand_seed, Rng64 base,
+                      double rate, float temp, float* out_sw, cudaStream_t st) {
+    int64_t threads = (n + kBootRun - 1) / kBootRun;
+    int64_t blocks = (threads + 255) / 256;
+    if (blocks < 1) return;
+    bootstrap_kernel<<<(unsigned)blocks, 256, 0, st>>>(mode, n, row_offset, rand_seed, base, rate,
+                                                       temp, out_sw);
+}
+
+// ---- MVS (bootstrap.rs:186-300): per 8192-row block a threshold from the
+// quickselect-style recursion with SEQUENTIAL f64 partial sums, then per row
+// p = min(1, sqrt(der^2 + lambda) / threshold), one draw per row with p > eps.
+
+constexpr int kMvsBlock = 8192;
+constexpr int kMvsThreads = 256;
+
+__device__ __forceinline__ double mvs_der_obj(double wd) { return sqrt(__dmul_rn(wd, wd)); }
+
+__global__ void __launch_bounds__(kMvsThreads) mvs_threshold_kernel(
+    int64_t n, const double* __restrict__ wd1, double lambda, double rate,
+    double* __restrict__ scratch, double* __restrict__ thresholds) {
+    extern __shared__ double msm[];
+    double* bufA = msm;
+    double* bufB = msm + kMvsBlock;
+    __shared__ int s_scan[40];
+    __shared__ double s_state[4];  // sum_small_cur, n_large_cur, result
+    __shared__ int s_ctl[4];       // len, which buffer/offset, done
+    (void)scratch;
+    const int64_t beg = (int64_t)blockIdx.x * kMvsBlock;
+    const int64_t end = beg + kMvsBlock < n ? beg + kMvsBlock : n;
+    const int bs = (int)(end - beg);
+    for (int k = threadIdx.x; k < bs; k += blockDim.x) {
+        double d = mvs_der_obj(wd1[beg + k]);
+        bufA[k] = sqrt(__dadd_rn(lambda, __dmul_rn(d, d)));
+    }
+    const double sample_size = (double)__fmul_rn((float)rate, (float)bs);
+    if (threadIdx.x == 0) {
+        s_state[0] = 0.0;
+        s_state[1] = 0.0;
+        s_ctl[0] = bs;
+        s_ctl[1] = 0;  // cur buffer = A, offset 0
+        s_ctl[2] = 0;  // done
+    }
+    __syncthreads();
+    for (;;) {
+        const int len = s_ctl[0];
+        double* cur = (s_ctl[1] & 1 ? bufB : bufA) + (s_ctl[1] >> 1);
+        double* oth = (s_ctl[1] & 1) ? bufA : bufB;
+        if (len == 0) {
+            if (threadIdx.x == 0) thresholds[blockIdx.x] = 0.0;
+            return;
+        }
+        const double thr = cur[0];
+        const int per = (len + blockDim.x - 1) / blockDim.x;
+        const int k0 = threadIdx.x * per;
+        const int k1 = k0 + per < len ? k0 + per : len;
+        int cs = 0, cm = 0, cl = 0;
+        for (int k = k0; k < k1; ++k) {
+            double c = cur[k];
+            if (c < thr) ++cs; else if (c <= thr) ++cm; else ++cl;
+        }
+        int ts, tl;
+        int ps = block_excl_scan<int>(cs, s_scan, &ts);
+        int pl = block_excl_scan<int>(cl, s_scan, &tl);
+        int tm_dummy;
+        (void)block_excl_scan<int>(cm, s_scan, &tm_dummy);
+        const int tm = tm_dummy;
+        for (int k = k0; k < k1; ++k) {
+            double c = cur[k];
+            if (c < thr) oth[ps++] = c;
+            else if (!(c <= thr)) oth[ts + pl++] = c;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            double sum_small_upd = 0.0;
+            for (int k = 0; k < ts; ++k) sum_small_upd = __dadd_rn(sum_small_upd, oth[k]);
+            const double s_cur = s_state[0], nl_cur = s_state[1];
+            const double nl_upd = (double)tl, n_mid = (double)tm;
+            const double sum_mid = __dmul_rn(n_mid, thr);
+            double est;
+            if (thr != 0.0)
+                est = __dadd_rn(__dadd_rn(__dadd_rn(__ddiv_rn(__dadd_rn(s_cur, sum_small_upd), thr), nl_cur),
+                                          nl_upd), n_mid);
+            else
+                est = INFINITY;
+            const int oth_id = (s_ctl[1] & 1) ? 0 : 1;
+            if (tl == len || ts == len) {
+                // no progress (a NaN pivot puts every element in `large`): stop
+                // with the pivot; the derivative kernel has flagged the NaN.
+                s_state[2] = thr;
+                s_ctl[2] = 1;
+            } else if (est > sample_size) {
+                if (tl > 0) {
+                    s_state[0] = __dadd_rn(__dadd_rn(s_cur, sum_mid), sum_small_upd);
+                    s_ctl[0] = tl;
+                    s_ctl[1] = oth_id | (ts << 1);
+                } else {
+                    double denom = __dsub_rn(sample_size, nl_cur);
+                    s_state[2] = denom != 0.0
+                                     ? __ddiv_rn(__dadd_rn(__dadd_rn(s_cur, sum_small_upd), sum_mid), denom)
+                                     : thr;
+                    s_ctl[2] = 1;
+                }
+            } else if (ts > 0) {
+                s_state[1] = __dadd_rn(__dadd_rn(nl_cur, nl_upd), n_mid);
+                s_ctl[0] = ts;
+                s_ctl[1] = oth_id;
+            } else {
+                double denom = __dsub_rn(__dsub_rn(__dsub_rn(sample_size, nl_cur), n_mid), nl_upd);
+                s_state[2] = denom != 0.0 ? __ddiv_rn(s_cur, denom) : thr;
+                s_ctl[2] = 1;
+            }
+        }
+        __syncthreads();
+        if (s_ctl[2]) {
+            if (threadIdx.x == 0) thresholds[blockIdx.x] = s_state[2];
+            return;
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kMvsThreads) mvs_weights_kernel(
+    int64_t n, int64_t row_offset, const double* __restrict__ wd1, double lambda,
+    uint64_t rand_seed, const double* __restrict__ thresholds, float* __restrict__ out) {
+    __shared__ int s_scan[40];
+    const int64_t beg = (int64_t)blockIdx.x * kMvsBlock;
+    const int64_t end = beg + kMvsBlock < n ? beg + kMvsBlock : n;
+    const int bs = (int)(end - beg);
+    const double thr = thresholds[blockIdx.x];
+    const int per = kMvsBlock / kMvsThreads;  // 32 rows per thread, contiguous
+    const int k0 = threadIdx.x * per;
+    int cnt = 0;
+    for (int k = k0; k < k0 + per && k < bs; ++k) {
+        double d = mvs_der_obj(wd1[beg + k]);
+        double x = sqrt(__dadd_rn(__dmul_rn(d, d), lambda));
+        double p = x > thr ? 1.0 : (thr > 0.0 ? __ddiv_rn(x, thr) : 0.0);
+        cnt += p > DBL_EPSILON;
+    }
+    int tot;
+    int idx = block_excl_scan<int>(cnt, s_scan, &tot);
+    const uint64_t gblk = (uint64_t)((row_offset + beg) / kMvsBlock);
+    Rng64 r = Rng64::from_seed(rand_seed + gblk);
+    r.advance(10 + (uint64_t)idx);
+    for (int k = k0; k < k0 + per && k < bs; ++k) {
+        double d = mvs_der_obj(wd1[beg + k]);
+        double x = sqrt(__dadd_rn(__dmul_rn(d, d), lambda));
+        double p = x > thr ? 1.0 : (thr > 0.0 ? __ddiv_rn(x, thr) : 0.0);
+        float w = 0.0f;
+        if (p > DBL_EPSILON) {
+            double weight = __ddiv_rn(1.0, p);
+            double u = real1(r);
+            w = __double2float_rn(__dmul_rn(weight, u < p ? 1.0 : 0.0));
+        }
+        out[beg + k] = w;
+    }
+}
+
+void launch_mvs(int64_t n, int64_t row_offset, const double* wd1, double lambda, double rate,
+                uint64_t rand_seed, double* scratch, double* thresholds, float* out_sw,
+                cudaStream_t st) {
+    int64_t blocks = (n + kMvsBlock - 1) / kMvsBlock;
+    if (blocks < 1) return;
+    size_t smem = sizeof(double) * 2 * kMvsBlock;
+    static bool attr = false;
+    if (!attr) {
+        cudaFuncSetAttribute(mvs_threshold_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem);
+        attr = true;
+    }
+    mvs_threshold_kernel<<<(unsigned)blocks, kMvsThreads, smem, st>>>(n, wd1, lambda, rate, scratch,
+                                                                       thresholds);
+    mvs_weights_kernel<<<(unsigned)blocks, kMvsThreads, 0, st>>>(n, row_offset, wd1, lambda,
+                                                                  rand_seed, thresholds, out_sw);
+}
+
+// ============================================================================
+// fused apply + derivatives + score channels (loss.rs:35-80, boosting.rs:7450-7732)
+// ============================================================================
+
+__device__ __forceinline__ void block_max4(double m[4], TreeState* ts) {
+    __shared__ double sm[4][32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        double v = m[c];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v = fmax(v, __shfl_xor_sync(kFull, v, o));
+        if (lane == 0) sm[c][warp] = v;
+    }
+    __syncthreads();
+    if (warp == 0) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            double v = lane < nw ? sm[c][lane] : 0.0;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) v = fmax(v, __shfl_xor_sync(kFull, v, o));
+            if (lane == 0 && v > 0.0) atomicMax(&ts->maxbits[c], (ull)__double_as_longlong(v));
+        }
+    }
+}
+
+__global__ void __launch_bounds__(256) der_kernel(
+    int64_t n, int loss, double* __restrict__ approx, const double* __restrict__ target,
+    const double* __restrict__ weight, const uint16_t* __restrict__ leaf,
+    const double* __restrict__ lrv, int s_mode, const float* __restrict__ sw32,
+    const double* __restrict__ sw64, double* __restrict__ wd1, double2* __restrict__ stats,
+    TreeState* ts, bool defer) {
+    double m[4] = {0.0, 0.0, 0.0, 0.0};
+    bool bad = false;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        double a = approx[i];
+        if (lrv) {
+            a = __dadd_rn(a, lrv[leaf[i]]);
+            approx[i] = a;
+        }
+        const double t = target[i];
+        double d1;
+        if (loss == 0) {
+            d1 = __dsub_rn(t, a);
+        } else {
+            const double e = exp(a);
+            const double p = __dsub_rn(1.0, __ddiv_rn(1.0, __dadd_rn(1.0, e)));
+            d1 = __dsub_rn(t, p);
+        }
+        const double w = weight ? weight[i] : 1.0;
+        const double wd = __dmul_rn(d1, w);
+        wd1[i] = wd;
+        m[2] = fmax(m[2], fabs(wd));
+        m[3] = fmax(m[3], fabs(w));
+        bad |= !isfinite(wd);
+        if (!defer) {
+            const double s = s_mode == 0 ? 1.0 : (s_mode == 1 ? (double)sw32[i] : sw64[i]);
+            const double g = __dmul_rn(wd, s), h = __dmul_rn(w, s);
+            stats[i] = make_double2(g, h);
+            m[0] = fmax(m[0], fabs(g));
+            m[1] = fmax(m[1], fabs(h));
+            bad |= !isfinite(g) || !isfinite(h);
+        }
+    }
+    if (bad) atomicOr(&ts->err, kErrOverflow);
+    block_max4(m, ts);
+}
+
+void launch_der(int64_t n, int loss, double* approx, const double* target, const double* weight,
+                const uint16_t* leaf, const double* lrv, int s_mode, const float* sw32,
+                const double* sw64, double* wd1, double2* stats, TreeState* ts, bool defer,
+                cudaStream_t st) {
+    int64_t blocks = (n + 255) / 256;
+    if (blocks > 148 * 8) blocks = 148 * 8;
+    if (blocks < 1) blocks = 1;
+    der_kernel<<<(unsigned)blocks, 256, 0, st>>>(n, loss, approx, target, weight, leaf, lrv, s_mode,
+                                                 sw32, sw64, wd1, stats, ts, defer);
+}
+
+__global__ void __launch_bounds__(256) stats_kernel(int64_t n, const double* __restrict__ wd1,
+                                                    const double* __restrict__ weight,
+                                                    const float* __restrict__ sw32,
+                                                    double2* __restrict__ stats, TreeState* ts) {
+    double m[4] = {0.0, 0.0, 0.0, 0.0};
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const double w = weight ? weight[i] : 1.0;
+        const double s = (double)sw32[i];
+        const double g = __dmul_rn(wd1[i], s), h = __dmul_rn(w, s);
+        stats[i] = make_double2(g, h);
+        m[0] = fmax(m[0], fabs(g));
+        m[1] = fmax(m[1], fabs(h));
+    }
+    block_max4(m, ts);
+}
+
+void launch_stats_from_sample(int64_t n, const double* wd1, const double* weight, const float* sw32,
+                              double2* stats, TreeState* ts, cudaStream_t st) {
+    int64_t blocks = (n + 255) / 256;
+    if (blocks > 148 * 8) blocks = 148 * 8;
+    if (blocks < 1) blocks = 1;
+    stats_kernel<<<(unsigned)blocks, 256, 0, st>>>(n, wd1, weight, sw32, stats, ts);
+}
+
+// Fixed-point scale per channel: 2^s with max|v| * n_total * 2^s < 2^62, so any
+// partial sum of rounded values stays below 2^63.
+__global__ void scales_kernel(TreeState* ts, int64_t n_total) {
+    if (threadIdx.x != 0) return;
+    for (int c = 0; c < 4; ++c) {
+        double m = __longlong_as_double((long long)ts->maxbits[c]);
+        int s = 0;
+        if (m > 0.0) {
+            int e;
+            frexp(m * (double)(n_total > 0 ? n_total : 1), &e);
+            s = 62 - e;
+            if (s > 1000) s = 1000;
+            if (s < -1000) s = -1000;
+        }
+        ts->sc.scale[c] = ldexp(1.0, s);
+        ts->sc.inv[c] = ldexp(1.0, -s);
+    }
+}
+
+void launch_scales(TreeState* ts, int64_t n_total, cudaStream_t st) {
+    scales_kernel<<<1, 32, 0, st>>>(ts, n_total);
+}
+
+__global__ void apply_kernel(int64_t n, double* __restrict__ approx, const uint16_t* __restrict__ leaf,
+                             const double* __restrict__ lrv) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x)
+        approx[i] = __dadd_rn(approx[i], lrv[leaf[i]]);
+}
+
+void launch_apply(int64_t n, double* approx, const uint16_t* leaf, const double* lrv,
+                  cudaStream_t st) {
+    int64_t blocks = (n + 255) / 256;
+    if (blocks > 148 * 8) blocks = 148 * 8;
+    if (blocks < 1) return;
+    apply_kernel<<<(unsigned)blocks, 256, 0, st>>>(n, approx, leaf, lrv);
+}
+
+// ============================================================================
+// histogram (the hot kernel)
+// ============================================================================
+//
+// Grid (chunk, feature tile).  A block owns one work item (rows of ONE leaf)
+// and one 32-feature tile; lane f of every warp owns feature tile*32+f, so the
+// 32 lanes of a shared-memory update always hit 32 different feature
+// histograms and never the same address.  Each warp reads a row's 32-byte tile
+// slice (one sector) and broadcasts the row's (g, h).  Channel values are
+// converted to int64 fixed point and accumulated with shared-memory atomics,
+// then merged into the global built histogram with int64 atomics: the sum is
+// exact and independent of ordering.
+
+void launch_zero(void* p, size_t bytes, cudaStream_t st) {
+    if (bytes) cudaMemsetAsync(p, 0, bytes, st);
+}
+
+template <bool kGather>
+__global__ void __launch_bounds__(kHistThreads) hist_kernel(
+    const uint8_t* __restrict__ bins_rm, int32_t F_pad, int32_t F, int32_t B,
+    const double2* __restrict__ stats, const uint32_t* __restrict__ perm,
+    const HistChunk* __restrict__ chunks, const uint32_t* __restrict__ n_chunks,
+    const TreeState* __restrict__ ts, ull* __restrict__ built) {
+    extern __shared__ ull hsm[];  // [kTile][B][2]
+    if (blockIdx.x >= *n_chunks) return;
+    const HistChunk ck = chunks[blockIdx.x];
+    const int tile = blockIdx.y;
+    const int cells = kTile * B * 2;
+    for (int k = threadIdx.x; k < cells; k += blockDim.x) hsm[k] = 0ull;
+    __syncthreads();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nwarps = blockDim.x >> 5;
+    const int f = tile * kTile + lane;
+    const bool active = f < F;
+    const double sg = ts->sc.scale[0], sh = ts->sc.scale[1];
+    const uint8_t* colp = bins_rm + f;
+    ull* my = hsm + lane * B * 2;
+    const uint32_t start = ck.start, len = ck.len;
+    uint32_t r = warp;
+    // 4 rows in flight per warp for memory-level parallelism
+    for (; r + 3 * nwarps < len; r += 4 * nwarps) {
+        uint32_t i[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            uint32_t j = start + r + u * nwarps;
+            i[u] = kGather ? __ldg(perm + j) : j;
+        }
+        double2 s[4];
+        uint32_t b[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            s[u] = __ldg(stats + i[u]);
+            b[u] = active ? __ldg(colp + (size_t)i[u] * F_pad) : 0u;
+        }
+        if (active) {
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                long long qg = __double2ll_rn(__dmul_rn(s[u].x, sg));
+                long long qh = __double2ll_rn(__dmul_rn(s[u].y, sh));
+                atomicAdd(my + 2 * b[u], (ull)qg);
+                atomicAdd(my + 2 * b[u] + 1, (ull)qh);
+            }
+        }
+    }
+    for (; r < len; r += nwarps) {
+        uint32_t j = start + r;
+        uint32_t i = kGather ? __ldg(perm + j) : j;
+        double2 s = __ldg(stats + i);
+        if (active) {
+            uint32_t b = __ldg(colp + (size_t)i * F_pad);
+            atomicAdd(my + 2 * b, (ull)__double2ll_rn(__dmul_rn(s.x, sg)));
+            atomicAdd(my + 2 * b + 1, (ull)__double2ll_rn(__dmul_rn(s.y, sh)));
+        }
+    }
+    __syncthreads();
+    const int nf = F - tile * kTile < kTile ? F - tile * kTile : kTile;
+    ull* out = built + ((size_t)ck.slot * F + (size_t)tile * kTile) * B * 2;
+    for (int k = threadIdx.x; k < nf * B * 2; k += blockDim.x) {
+        ull v = hsm[k];
+        if (v) atomicAdd(out + k, v);
+    }
+}
+
+void launch_hist(const uint8_t* bins_rm, int32_t F_pad, int32_t F, int32_t B,
+                 const double2* stats, const uint32_t* perm, const HistChunk* chunks,
+                 const uint32_t* n_chunks, uint32_t max_chunks, const TreeState* ts, ull* built,
+                 cudaStream_t st) {
+    if (max_chunks == 0) return;
+    size_t smem = sizeof(ull) * kTile * B * 2;
+    static bool attr = false;
+    if (!attr) {
+        cudaFuncSetAttribute(hist_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        cudaFuncSetAttribute(hist_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        attr = true;
+    }
+    dim3 grid(max_chunks, (unsigned)((F + kTile - 1) / kTile));
+    if (perm)
+        hist_kernel<true><<<grid, kHistThreads, smem, st>>>(bins_rm, F_pad, F, B, stats, perm, chunks,
+                                                             n_chunks, ts, built);
+    else
+        hist_kernel<false><<<grid, kHistThreads, smem, st>>>(bins_rm, F_pad, F, B, stats, perm,
+                                                              chunks, n_chunks, ts, built);
+}
+
+// Work list for the level: level 0 = all rows (identity order) in one slot;
+// level l >= 1 = for each parent p the smaller child's leaf-sorted segment
+// into slot p, cut into kChunkRows pieces.
+__global__ void make_chunks_kernel(int level, uint32_t* __restrict__ seg_off,
+                                   uint32_t* __restrict__ seg_cnt,
+                                   const uint8_t* __restrict__ small_side, int64_t n0,
+                                   HistChunk* __restrict__ chunks, uint32_t* __restrict__ n_chunks,
+                                   TreeState* ts) {
+    __shared__ uint32_t s_scan[40];
+    if (level == 0) {
+        uint32_t nch = (uint32_t)((n0 + kChunkRows - 1) / kChunkRows);
+        for (uint32_t k = threadIdx.x; k < nch; k += blockDim.x) {
+            uint32_t st = k * kChunkRows;
+            uint32_t ln = (uint32_t)(n0 - st < kChunkRows ? n0 - st : kChunkRows);
+            chunks[k] = HistChunk{0u, st, ln, 0u};
+        }
+        if (threadIdx.x == 0) {
+            *n_chunks = nch;
+            seg_off[0] = 0u;  // level 0: one segment holding every row
+            seg_cnt[0] = (uint32_t)n0;
+            ts->hist_rows[0] = (uint32_t)n0;
+        }
+        return;
+    }
+    const uint32_t half = 1u << (level - 1);
+    const uint32_t per = (half + blockDim.x - 1) / blockDim.x;
+    const uint32_t p0 = threadIdx.x * per;
+    uint32_t cnt = 0, rows = 0;
+    for (uint32_t p = p0; p < p0 + per && p < half; ++p) {
+        uint32_t c = small_side[p] ? p + half : p;
+        cnt += (seg_cnt[c] + kChunkRows - 1) / kChunkRows;
+        rows += seg_cnt[c];
+    }
+    uint32_t tot, rows_tot;
+    uint32_t base = block_excl_scan<uint32_t>(cnt, s_scan, &tot);
+    (void)block_excl_scan<uint32_t>(rows, s_scan, &rows_tot);
+    for (uint32_t p = p0; p < p0 + per && p < half; ++p) {
+        uint32_t c = small_side[p] ? p + half : p;
+        uint32_t off = seg_off[c], ln = seg_cnt[c];
+        for (uint32_t st = 0; st < ln; st += kChunkRows) {
+            chunks[base++] = HistChunk{p, off + st, ln - st < (uint32_t)kChunkRows ? ln - st : (uint32_t)kChunkRows, 0u};
+        }
+    }
+    if (threadIdx.x == 0) {
+        *n_chunks = tot;
+        ts->hist_rows[level] = rows_tot;
+    }
+}
+
+void launch_make_chunks(int level, uint32_t* seg_off, uint32_t* seg_cnt,
+                        const uint8_t* small_side, int64_t n_level0, HistChunk* chunks,
+                        uint32_t* n_chunks, TreeState* ts, cudaStream_t st) {
+    make_chunks_kernel<<<1, 1024, 0, st>>>(level, seg_off, seg_cnt, small_side, n_level0, chunks,
+                                           n_chunks, ts);
+}
+
+// ============================================================================
+// derive siblings + bin prefix: cur[q][f][*] = inclusive prefix over bins.
+// Level 0: prefix(built[0]).  Level l: parent p = q mod 2^(l-1); the built child
+// of p is copied, the other is prev[p] - prefix(built[p]) (exact integers; the
+// subtraction trick of tree.rs:1075-1131 applied to prefix sums, which are linear).
+// One warp per (leaf, feature) row.
+// ============================================================================
+__global__ void derive_prefix_kernel(int level, int32_t F, int32_t B, const ull* __restrict__ built,
+                                     const ull* __restrict__ prev, ull* __restrict__ cur,
+                                     const uint8_t* __restrict__ small_side) {
+    const int lane = threadIdx.x & 31;
+    const int64_t row = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+    const int64_t Q = 1ll << level;
+    if (row >= Q * F) return;
+    const int64_t q = row / F;
+    const int f = (int)(row % F);
+    int64_t p = 0;
+    bool is_built = true;
+    if (level > 0) {
+        const int64_t half = Q >> 1;
+        p = q & (half - 1);
+        is_built = ((q >> (level - 1)) & 1) == (int64_t)small_side[p];
+    }
+    const ull* src = built + ((size_t)p * F + f) * B * 2;
+    const ull* par = (level > 0) ? prev + ((size_t)p * F + f) * B * 2 : nullptr;
+    ull* dst = cur + ((size_t)q * F + f) * B * 2;
+    const int K = (B + 31) / 32;
+    const int b0 = lane * K;
+    long long lg = 0, lh = 0;
+    for (int k = 0; k < K; ++k) {
+        int b = b0 + k;
+        if (b < B) {
+            lg += (long long)src[2 * b];
+            lh += (long long)src[2 * b + 1];
+        }
+    }
+    long long ig = warp_incl_scan<long long>(lg), ih = warp_incl_scan<long long>(lh);
+    long long ag = ig - lg, ah = ih - lh;
+    for (int k = 0; k < K; ++k) {
+        int b = b0 + k;
+        if (b < B) {
+            ag += (long long)src[2 * b];
+            ah += (long long)src[2 * b + 1];
+            long long og = ag, oh = ah;
+            if (!is_built) {
+                og = (long long)par[2 * b] - ag;
+                oh = (long long)par[2 * b + 1] - ah;
+            }
+            dst[2 * b] = (ull)og;
+            dst[2 * b + 1] = (ull)oh;
+        }
+    }
+}
+
+void launch_derive_prefix(int level, int32_t F, int32_t B, const ull* built, const ull* prev,
+                          ull* cur, const uint8_t* small_side, cudaStream_t st) {
+    int64_t rows = (1ll << level) * F;
+    int64_t blocks = (rows * 32 + 255) / 256;
+    derive_prefix_kernel<<<(unsigned)blocks, 256, 0, st>>>(level, F, B, built, prev, cur, small_side);
+}
+
+// ============================================================================
+// scoring (score.rs:39-265, histogram.rs:1007-1171) + argmax (tree.rs:355-366)
+// One block per feature, one thread per candidate border; the 2Q children are
+// folded in the CPU's canonical order (false children 0..Q-1, then true).
+// The last block to finish reduces the per-feature winners (no spin wait).
+// ============================================================================
+__global__ void __launch_bounds__(256) score_kernel(int level, int32_t F, int32_t B,
+                                                    const ull* __restrict__ cur,
+                                                    const int32_t* __restrict__ border_counts,
+                                                    double l2, int score_fn,
+                                                    double* __restrict__ feat_score,
+                                                    int32_t* __restrict__ feat_bin, TreeState* ts) {
+    __shared__ double s_sc[32];
+    __shared__ int s_bi[32];
+    __shared__ bool s_last;
+    const int f = blockIdx.x;
+    const int nb = border_counts[f];
+    const int Q = 1 << level;
+    const double ig = ts->sc.inv[0], ih = ts->sc.inv[1];
+    double best = -INFINITY;
+    int bbin = 0x7fffffff;
+    for (int b = threadIdx.x; b < nb; b += blockDim.x) {
+        double num = 0.0, den = 1e-100;
+        for (int side = 0; side < 2; ++side) {
+            for (int q = 0; q < Q; ++q) {
+                const ull* row = cur + ((size_t)q * F + f) * B * 2;
+                long long pg = (long long)row[2 * b], ph = (long long)row[2 * b + 1];
+                if (side) {
+                    pg = (long long)row[2 * (B - 1)] - pg;
+                    ph = (long long)row[2 * (B - 1) + 1] - ph;
+                }
+                const double swd = __dmul_rn((double)pg, ig);
+                const double sw = __dmul_rn((double)ph, ih);
+                const double avg = sw > 0.0 ? __ddiv_rn(swd, __dadd_rn(sw, l2)) : 0.0;
+                num = __dadd_rn(num, __dmul_rn(avg, swd));
+                if (score_fn == 0) den = __dadd_rn(den, __dmul_rn(__dmul_rn(avg, avg), sw));
+            }
+        }
+        double s = score_fn == 0 ? __ddiv_rn(num, sqrt(den)) : num;
+        s = nan_to_neg_inf(s);
+        if (better(s, b, best, bbin)) {
+            best = s;
+            bbin = b;
+        }
+    }
+    // block argmax
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        double os = __shfl_xor_sync(kFull, best, o);
+        int ob = __shfl_xor_sync(kFull, bbin, o);
+        if (better(os, ob, best, bbin)) { best = os; bbin = ob; }
+    }
+    if (lane == 0) { s_sc[warp] = best; s_bi[warp] = bbin; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < nw; ++w)
+            if (better(s_sc[w], s_bi[w], best, bbin)) { best = s_sc[w]; bbin = s_bi[w]; }
+        feat_score[f] = best;
+        feat_bin[f] = bbin;
+        __threadfence();
+        unsigned done = atomicAdd(&ts->score_done, 1u);
+        s_last = (done == gridDim.x - 1);
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    // final reduction over features, lowest feature on ties
+    double fb = -INFINITY;
+    int fi = 0x7fffffff;
+    for (int ff = threadIdx.x; ff < F; ff += blockDim.x) {
+        double s = ((volatile double*)feat_score)[ff];
+        if (better(s, ff, fb, fi)) { fb = s; fi = ff; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        double os = __shfl_xor_sync(kFull, fb, o);
+        int oi = __shfl_xor_sync(kFull, fi, o);
+        if (better(os, oi, fb, fi)) { fb = os; fi = oi; }
+    }
+    __syncthreads();
+    if (lane == 0) { s_sc[warp] = fb; s_bi[warp] = fi; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < nw; ++w)
+            if (better(s_sc[w], s_bi[w], fb, fi)) { fb = s_sc[w]; fi = s_bi[w]; }
+        SplitRec rec;
+        if (fi == 0x7fffffff || fb == -INFINITY) {
+            rec.feature = -1;
+            rec.bin = -1;
+            rec.score = -INFINITY;
+            atomicOr(&ts->err, kErrNoCandidate);
+        } else {
+            rec.feature = fi;
+            rec.bin = ((volatile int32_t*)feat_bin)[fi];
+            rec.score = fb;
+        }
+        ts->split[level] = rec;
+        ts->score_done = 0;
+    }
+}
+
+void launch_score(int level, int32_t F, int32_t B, const ull* cur, const int32_t* border_counts,
+                  double l2, int score_fn, double* feat_score, int32_t* feat_bin, TreeState* ts,
+                  cudaStream_t st) {
+    score_kernel<<<(unsigned)F, 128, 0, st>>>(level, F, B, cur, border_counts, l2, score_fn,
+                                              feat_score, feat_bin, ts);
+}
+
+// ============================================================================
+// partition: stable per-segment split of the leaf-sorted row order so the
+// next level can gather each child's rows contiguously.
+//  P1 (count): per tile of kPartTile positions: true-flag count, and for each
+//     segment that starts / ends inside the tile the in-tile prefix there.
+//  P2 (scan):  tile offsets, per-segment true counts, child counts, next
+//     segment table.
+//  P3 (scatter): destination of every position, new leaf ids.
+// ============================================================================
+
+struct PartView {
+    const uint8_t* col;
+    int32_t bin;
+};
+
+__device__ __forceinline__ PartView part_view(const TreeState* ts, int level, const uint8_t* bins_fm,
+                                              int64_t n_stride) {
+    SplitRec s = ts->split[level];
+    PartView v;
+    int f = s.feature < 0 ? 0 : s.feature;
+    v.col = bins_fm + (int64_t)f * n_stride;
+    v.bin = s.feature < 0 ? 0x7fffffff : s.bin;
+    return v;
+}
+
+__global__ void __launch_bounds__(kPartThreads) part_count_kernel(
+    int level, int64_t n, const uint8_t* __restrict__ bins_fm, int64_t n_stride,
+    const uint32_t* __restrict__ perm, const uint16_t* __restrict__ leaf,
+    uint32_t* __restrict__ seg_start_blk, uint32_t* __restrict__ seg_start_part,
+    uint32_t* __restrict__ seg_end_blk, uint32_t* __restrict__ seg_end_part,
+    uint32_t* __restrict__ blk_true, const TreeState* __restrict__ ts) {
+    __shared__ uint32_t s_idx[kPartTile];
+    __shared__ uint32_t s_scan[40];
+    const PartView pv = part_view(ts, level, bins_fm, n_stride);
+    const uint32_t mask = (1u << level) - 1u;
+    const int64_t base = (int64_t)blockIdx.x * kPartTile;
+    for (int k = threadIdx.x; k < kPartTile; k += blockDim.x) {
+        int64_t j = base + k;
+        s_idx[k] = j < n ? (perm ? perm[j] : (uint32_t)j) : 0xffffffffu;
+    }
+    __syncthreads();
+    const int k0 = threadIdx.x * kPartItems;
+    uint32_t flags = 0, qs[kPartItems];
+    int cnt = 0;
+#pragma unroll
+    for (int u = 0; u < kPartItems; ++u) {
+        uint32_t i = s_idx[k0 + u];
+        if (i != 0xffffffffu) {
+            uint32_t fl = (int32_t)pv.col[i] > pv.bin;
+            flags |= fl << u;
+            cnt += fl;
+            qs[u] = level ? (leaf[i] & mask) : 0u;
+        } else {
+            qs[u] = 0xffffffffu;
+        }
+    }
+    // leaf of the previous position (for segment-start detection)
+    uint32_t q_prev;
+    {
+        int64_t jp = base + k0 - 1;
+        if (jp < 0 || jp >= n) q_prev = 0xfffffffeu;  // no previous row, or no rows in this thread
+        else {
+            uint32_t ip = (k0 > 0) ? s_idx[k0 - 1] : (perm ? perm[jp] : (uint32_t)jp);
+            q_prev = level ? (leaf[ip] & mask) : 0u;
+        }
+    }
+    uint32_t q_next;
+    {
+        int64_t jn = base + k0 + kPartItems;
+        if (jn >= n) q_next = 0xfffffffdu;
+        else {
+            uint32_t in = (k0 + kPartItems < kPartTile) ? s_idx[k0 + kPartItems] : (perm ? perm[jn] : (uint32_t)jn);
+            q_next = level ? (leaf[in] & mask) : 0u;
+        }
+    }
+    uint32_t tot;
+    uint32_t excl = block_excl_scan<uint32_t>((uint32_t)cnt, s_scan, &tot);
+    uint32_t run = excl;
+#pragma unroll
+    for (int u = 0; u < kPartItems; ++u) {
+        uint32_t q = qs[u];
+        if (q == 0xffffffffu) break;
+        uint32_t before = (u == 0) ? q_prev : qs[u - 1];
+        uint32_t fl = (flags >> u) & 1u;
+        if (q != before) {
+            seg_start_blk[q] = blockIdx.x;
+            seg_start_part[q] = run;
+        }
+        run += fl;
+        uint32_t after = (u + 1 < kPartItems && qs[u + 1] != 0xffffffffu) ? qs[u + 1]
+                         : (u + 1 < kPartItems ? 0xfffffffcu : q_next);
+        if (q != after) {
+            seg_end_blk[q] = blockIdx.x;
+            seg_end_part[q] = run;  // inclusive
+        }
+    }
+    if (threadIdx.x == 0) blk_true[blockIdx.x] = tot;
+}
+
+// Single block: tile offsets (in place), per-segment T_start and false count,
+// child counts and the next level's segment table.
+__global__ void __launch_bounds__(1024) part_scan_kernel(
+    int level, uint32_t n_tiles, uint32_t* __restrict__ blk_true,
+    const uint32_t* __restrict__ seg_off, const uint32_t* __restrict__ seg_cnt,
+    const uint32_t* __restrict__ seg_start_blk, const uint32_t* __restrict__ seg_start_part,
+    const uint32_t* __restrict__ seg_end_blk, const uint32_t* __restrict__ seg_end_part,
+    uint32_t* __restrict__ t_start, uint32_t* __restrict__ f_cnt, uint32_t* __restrict__ child_cnt,
+    uint32_t* __restrict__ seg_off_next, uint32_t* __restrict__ seg_cnt_next) {
+    __shared__ uint32_t s_scan[40];
+    const uint32_t per = (n_tiles + blockDim.x - 1) / blockDim.x;
+    const uint32_t t0 = threadIdx.x * per;
+    uint32_t loc = 0;
+    for (uint32_t t = t0; t < t0 + per && t < n_tiles; ++t) loc += blk_true[t];
+    uint32_t tot;
+    uint32_t off = block_excl_scan<uint32_t>(loc, s_scan, &tot);
+    for (uint32_t t = t0; t < t0 + per && t < n_tiles; ++t) {
+        uint32_t v = blk_true[t];
+        blk_true[t] = off;
+        off += v;
+    }
+    __syncthreads();
+    const uint32_t Q = 1u << level;
+    for (uint32_t q = threadIdx.x; q < Q; q += blockDim.x) {
+        uint32_t cnt = seg_cnt[q];
+        uint32_t ts = 0, tt = 0;
+        if (cnt > 0) {
+            ts = blk_true[seg_start_blk[q]] + seg_start_part[q];
+            uint32_t te = blk_true[seg_end_blk[q]] + seg_end_part[q];
+            tt = te - ts;
+        }
+        uint32_t fc = cnt - tt;
+        t_start[q] = ts;
+        f_cnt[q] = fc;
+        child_cnt[q] = fc;
+        child_cnt[q + Q] = tt;
+        seg_off_next[q] = seg_off[q];
+        seg_cnt_next[q] = fc;
+        seg_off_next[q + Q] = seg_off[q] + fc;
+        seg_cnt_next[q + Q] = tt;
+    }
+}
+
+__global__ void __launch_bounds__(kPartThreads) part_scatter_kernel(
+    int level, int64_t n, const uint8_t* __restrict__ bins_fm, int64_t n_stride,
+    const uint32_t* __restrict__ perm, uint32_t* __restrict__ perm_next, uint16_t* __restrict__ leaf,
+    const uint32_t* __restrict__ seg_off, const uint32_t* __restrict__ blk_off,
+    const uint32_t* __restrict__ t_start, const uint32_t* __restrict__ f_cnt,
+    const TreeState* __restrict__ ts) {
+    __shared__ uint32_t s_idx[kPartTile];
+    __shared__ uint32_t s_scan[40];
+    const PartView pv = part_view(ts, level, bins_fm, n_stride);
+    const uint32_t mask = (1u << level) - 1u;
+    const int64_t base = (int64_t)blockIdx.x * kPartTile;
+    for (int k = threadIdx.x; k < kPartTile; k += blockDim.x) {
+        int64_t j = base + k;
+        s_idx[k] = j < n ? (perm ? perm[j] : (uint32_t)j) : 0xffffffffu;
+    }
+    __syncthreads();
+    const int k0 = threadIdx.x * kPartItems;
+    uint32_t flags = 0;
+    int cnt = 0;
+#pragma unroll
+    for (int u = 0; u < kPartItems; ++u) {
+        uint32_t i = s_idx[k0 + u];
+        if (i != 0xffffffffu) {
+            uint32_t fl = (int32_t)pv.col[i] > pv.bin;
+            flags |= fl << u;
+            cnt += fl;
+        }
+    }
+    uint32_t excl = block_excl_scan<uint32_t>((uint32_t)cnt, s_scan, nullptr);
+    uint32_t T = blk_off[blockIdx.x] + excl;
+#pragma unroll
+    for (int u = 0; u < kPartItems; ++u) {
+        uint32_t i = s_idx[k0 + u];
+        if (i == 0xffffffffu) break;
+        uint32_t j = (uint32_t)(base + k0 + u);
+        uint32_t q = level ? (leaf[i] & mask) : 0u;
+        uint32_t fl = (flags >> u) & 1u;
+        uint32_t rel = T - t_start[q];
+        uint32_t dest = fl ? seg_off[q] + f_cnt[q] + rel : j - rel;
+        perm_next[dest] = i;
+        leaf[i] = (uint16_t)(q | (fl << level));
+        T += fl;
+    }
+}
+
+void launch_partition(int level, int64_t n, const uint8_t* bins_fm, int64_t n_stride,
+                      const uint32_t* perm, uint32_t* perm_next, uint16_t* leaf, uint32_t* seg_off,
+                      uint32_t* seg_cnt, uint32_t* scratch, uint32_t* seg_start_blk,
+                      uint32_t* seg_start_part, uint32_t* blk_true, uint32_t* child_cnt,
+                      TreeState* ts, cudaStream_t st) {
+    // scratch layout: [seg_end_blk | seg_end_part | t_start | f_cnt | seg_off_next | seg_cnt_next]
+    const uint32_t Qmax = 1u << 16;
+    uint32_t* seg_end_blk = scratch;
+    uint32_t* seg_end_part = scratch + Qmax;
+    uint32_t* t_start = scratch + 2 * Qmax;
+    uint32_t* f_cnt = scratch + 3 * Qmax;
+    uint32_t* seg_off_next = scratch + 4 * Qmax;
+    uint32_t* seg_cnt_next = scratch + 6 * Qmax;
+    const uint32_t tiles = (uint32_t)((n + kPartTile - 1) / kPartTile);
+    if (tiles == 0) return;
+    part_count_kernel<<<tiles, kPartThreads, 0, st>>>(level, n, bins_fm, n_stride, perm, leaf,
+                                                       seg_start_blk, seg_start_part, seg_end_blk,
+                                                       seg_end_part, blk_true, ts);
+    part_scan_kernel<<<1, 1024, 0, st>>>(level, tiles, blk_true, seg_off, seg_cnt, seg_start_blk,
+                                         seg_start_part, seg_end_blk, seg_end_part, t_start, f_cnt,
+                                         child_cnt, seg_off_next, seg_cnt_next);
+    part_scatter_kernel<<<tiles, kPartThreads, 0, st>>>(level, n, bins_fm, n_stride, perm, perm_next,
+                                                         leaf, seg_off, blk_true, t_start, f_cnt, ts);
+    const uint32_t Qn = 2u << level;
+    cudaMemcpyAsync(seg_off, seg_off_next, sizeof(uint32_t) * Qn, cudaMemcpyDeviceToDevice, st);
+    cudaMemcpyAsync(seg_cnt, seg_cnt_next, sizeof(uint32_t) * Qn, cudaMemcpyDeviceToDevice, st);
+}
+
+// small_side[q] = 1 when the TRUE child of q is the one to build (<= rows, as
+// the CPU's n_true <= n_false rule, tree.rs:1111).
+__global__ void small_side_kernel(int level_next, const uint32_t* __restrict__ child_cnt,
+                                  uint8_t* __restrict__ small_side) {
+    const uint32_t half = 1u << (level_next - 1);
+    for (uint32_t q = blockIdx.x * blockDim.x + threadIdx.x; q < half; q += gridDim.x * blockDim.x)
+        small_side[q] = child_cnt[q + half] <= child_cnt[q] ? 1 : 0;
+}
+
+void launch_small_side(int level_next, const uint32_t* child_cnt_global, uint8_t* small_side,
+                       cudaStream_t st) {
+    const uint32_t half = 1u << (level_next - 1);
+    unsigned blocks = (half + 255) / 256;
+    small_side_kernel<<<blocks, 256, 0, st>>>(level_next, child_cnt_global, small_side);
+}
+
+// ============================================================================
+// last level: route + unsampled leaf sums (boosting.rs:2470-2517 Gradient
+// leaves over the full w*der1 / w channels), exact int64.
+// ============================================================================
+__global__ void __launch_bounds__(256) route_leafsum_kernel(
+    int level, int64_t n, const uint8_t* __restrict__ bins_fm, int64_t n_stride,
+    uint16_t* __restrict__ leaf, const double* __restrict__ wd1, const double* __restrict__ weight,
+    int depth, const TreeState* __restrict__ ts, ull* __restrict__ leaf_sums) {
+    extern __shared__ ull lsm[];
+    const int L = 1 << depth;
+    const bool use_smem = depth <= 10;
+    if (use_smem) {
+        for (int k = threadIdx.x; k < 2 * L; k += blockDim.x) lsm[k] = 0ull;
+        __syncthreads();
+    }
+    const PartView pv = part_view(ts, level, bins_fm, n_stride);
+    const uint32_t mask = (1u << level) - 1u;
+    const double sd = ts->sc.scale[2], sw = ts->sc.scale[3];
+    ull* acc = use_smem ? lsm : leaf_sums;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        uint32_t q = (level ? (leaf[i] & mask) : 0u) | ((uint32_t)((int32_t)pv.col[i] > pv.bin) << level);
+        leaf[i] = (uint16_t)q;
+        const double w = weight ? weight[i] : 1.0;
+        atomicAdd(acc + 2 * q, (ull)__double2ll_rn(__dmul_rn(wd1[i], sd)));
+        atomicAdd(acc + 2 * q + 1, (ull)__double2ll_rn(__dmul_rn(w, sw)));
+    }
+    if (use_smem) {
+        __syncthreads();
+        for (int k = threadIdx.x; k < 2 * L; k += blockDim.x)
+            if (lsm[k]) atomicAdd(leaf_sums + k, lsm[k]);
+    }
+}
+
+void launch_route_leafsum(int level, int64_t n, const uint8_t* bins_fm, int64_t n_stride,
+                          uint16_t* leaf, const double* wd1, const double* weight, int depth,
+                          TreeState* ts, ull* leaf_sums, cudaStream_t st) {
+    int64_t blocks = (n + 255) / 256;
+    if (blocks > 148 * 4) blocks = 148 * 4;
+    if (blocks < 1) blocks = 1;
+    size_t smem = depth <= 10 ? sizeof(ull) * 2 * (1 << depth) : 0;
+    route_leafsum_kernel<<<(unsigned)blocks, 256, smem, st>>>(level, n, bins_fm, n_stride, leaf, wd1,
+                                                               weight, depth, ts, leaf_sums);
+}
+
+// Gradient leaf delta calc_average(sum w*der1, sum w, scaled_l2) (leaf.rs:161-199),
+// then x learning rate for the resident approx (normalize_leaf_values).
+__global__ void leaf_values_kernel(int depth, const ull* __restrict__ leaf_sums, double l2, double lr,
+                                   const TreeState* __restrict__ ts, double* __restrict__ raw,
+                                   double* __restrict__ lrv) {
+    const int L = 1 << depth;
+    const double id = ts->sc.inv[2], iw = ts->sc.inv[3];
+    for (int q = blockIdx.x * blockDim.x + threadIdx.x; q < L; q += gridDim.x * blockDim.x) {
+        const double sd = __dmul_rn((double)(long long)leaf_sums[2 * q], id);
+        const double sw = __dmul_rn((double)(long long)leaf_sums[2 * q + 1], iw);
+        const double v = sw > 0.0 ? __ddiv_rn(sd, __dadd_rn(sw, l2)) : 0.0;
+        raw[q] = v;
+        lrv[q] = __dmul_rn(v, lr);
+    }
+}
+
+void launch_leaf_values(int depth, int n_splits_expected, const ull* leaf_sums, double l2, double lr,
+                        TreeState* ts, double* leaf_raw, double* leaf_lrv, cudaStream_t st) {
+    (void)n_splits_expected;
+    int L = 1 << depth;
+    leaf_values_kernel<<<(L + 255) / 256, 256, 0, st>>>(depth, leaf_sums, l2, lr, ts, leaf_raw,
+                                                        leaf_lrv);
+}
+
+__global__ void leaf_export_kernel(int64_t n, const uint16_t* __restrict__ leaf, void* out, int bytes) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        uint16_t v = leaf[i];
+        if (bytes == 1) ((uint8_t*)out)[i] = (uint8_t)v;
+        else if (bytes == 2) ((uint16_t*)out)[i] = v;
+        else ((uint32_t*)out)[i] = v;
+    }
+}
+
+void launch_leaf_export(int64_t n, const uint16_t* leaf, void* out, int bytes, cudaStream_t st) {
+    int64_t blocks = (n + 255) / 256;
+    if (blocks > 148 * 8) blocks = 148 * 8;
+    if (blocks < 1) return;
+    leaf_export_kernel<<<(unsigned)blocks, 256, 0, st>>>(n, leaf, out, bytes);
+}
+
+__global__ void gradients_kernel(int64_t n, int loss, const double* __restrict__ approx,
+                                 const double* __restrict__ target, double* __restrict__ d1,
+                                 double* __restrict__ d2) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const double a = approx[i], t = target[i];
+        if (loss == 0) {
+            d1[i] = __dsub_rn(t, a);
+            if (d2) d2[i] = -1.0;
+        } else {
+            const double e = exp(a);
+            const double p = __dsub_rn(1.0, __ddiv_rn(1.0, __dadd_rn(1.0, e)));
+            d1[i] = __dsub_rn(t, p);
+            if (d2) d2[i] = -__dmul_rn(p, __dsub_rn(1.0, p));
+        }
+    }
+}
+
+void launch_gradients(int64_t n, int loss, const double* approx, const double* target, double* d1,
+                      double* d2, cudaStream_t st) {
+    int64_t blocks = (n + 255) / 256;
+    if (blocks > 148 * 8) blocks = 148 * 8;
+    if (blocks < 1) return;
+    gradients_kernel<<<(unsigned)blocks, 256, 0, st>>>(n, loss, approx, target, d1, d2);
+}
+
+}  // namespace cbgpu

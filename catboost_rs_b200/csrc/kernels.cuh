@@ -1,0 +1,116 @@
+// kernels.cuh -- device kernels of the B200 oblivious-tree path and their launchers.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "cbgpu_common.cuh"
+
+namespace cbgpu {
+
+using ull = unsigned long long;
+
+// Fixed-point scales for the four int64 accumulation channels:
+// 0 = score der (g), 1 = score weight (h), 2 = leaf der (w*der1), 3 = leaf weight (w).
+struct Scales {
+    double scale[4];
+    double inv[4];
+};
+
+// One histogram work item: rows [start, start+len) of the (leaf-sorted) order
+// go into built-histogram slot `slot`.
+struct HistChunk {
+    uint32_t slot;
+    uint32_t start;
+    uint32_t len;
+    uint32_t pad;
+};
+
+// The split chosen at one level.
+struct SplitRec {
+    int32_t feature;
+    int32_t bin;
+    double score;
+};
+
+// Per-tree device-side results (one D2H per tree).
+struct TreeState {
+    SplitRec split[16];
+    uint32_t err;
+    uint32_t score_done;   // last-block-done counter of the score kernel
+    uint32_t pad[2];
+    uint32_t hist_rows[16];  // rows histogrammed at each level (the smaller children)
+    ull maxbits[4];        // bit patterns of max |channel| (non-negative doubles)
+    Scales sc;
+};
+
+constexpr int kTile = 32;          // features per histogram tile (one per lane)
+constexpr int kHistThreads = 256;  // 8 warps
+constexpr int kChunkRows = 8192;   // rows per histogram work item
+constexpr int kPartThreads = 256;
+constexpr int kPartItems = 16;     // positions per thread in the partition kernels
+constexpr int kPartTile = kPartThreads * kPartItems;
+constexpr int kBootRun = 8;        // consecutive rows per thread in the bootstrap kernel
+
+// ---- begin: quantization / layout ------------------------------------------
+void launch_quantize_column(const float* col, int64_t n, const double* borders, int32_t nb,
+                            uint8_t* out_fm_row, uint32_t* err, cudaStream_t st);
+void launch_u32_to_u8_column(const uint32_t* col, int64_t n, int32_t n_bins, uint8_t* out_fm_row,
+                             uint32_t* err, cudaStream_t st);
+void launch_transpose_fm_to_rm(const uint8_t* fm, int64_t n, int64_t n_stride, int32_t F,
+                               uint8_t* rm, int32_t F_pad, cudaStream_t st);
+void launch_transpose_rm_to_fm(const uint8_t* rm, int64_t n, int32_t F, int32_t F_src,
+                               uint8_t* fm, int64_t n_stride, cudaStream_t st);
+
+// ---- per tree: bootstrap, derivatives, scales -------------------------------
+// mode: 1 = Bayesian (rand_seed, temp), 2 = Bernoulli (base state, rate)
+void launch_bootstrap(int mode, int64_t n, int64_t row_offset, uint64_t rand_seed, Rng64 base,
+                      double rate, float temp, float* out_sw, cudaStream_t st);
+void launch_mvs(int64_t n, int64_t row_offset, const double* wd1, double lambda, double rate,
+                uint64_t rand_seed, double* scratch, double* thresholds, float* out_sw,
+                cudaStream_t st);
+// s_mode: 0 = none (weights 1), 1 = f32 device sample, 2 = f64 host sample
+void launch_der(int64_t n, int loss, double* approx, const double* target, const double* weight,
+                const uint16_t* leaf, const double* pending_lrv, int s_mode, const float* sw32,
+                const double* sw64, double* wd1, double2* stats, TreeState* ts, bool defer_stats,
+                cudaStream_t st);
+void launch_stats_from_sample(int64_t n, const double* wd1, const double* weight, const float* sw32,
+                              double2* stats, TreeState* ts, cudaStream_t st);
+void launch_scales(TreeState* ts, int64_t n_total, cudaStream_t st);
+void launch_apply(int64_t n, double* approx, const uint16_t* leaf, const double* lrv,
+                  cudaStream_t st);
+
+// ---- per level ---------------------------------------------------------------
+void launch_zero(void* p, size_t bytes, cudaStream_t st);
+void launch_hist(const uint8_t* bins_rm, int32_t F_pad, int32_t F, int32_t B,
+                 const double2* stats, const uint32_t* perm, const HistChunk* chunks,
+                 const uint32_t* n_chunks, uint32_t max_chunks, const TreeState* ts, ull* built,
+                 cudaStream_t st);
+// level 0 also initialises the single all-rows segment (seg_off[0] = 0, seg_cnt[0] = n).
+void launch_make_chunks(int level, uint32_t* seg_off, uint32_t* seg_cnt,
+                        const uint8_t* small_side, int64_t n_level0, HistChunk* chunks,
+                        uint32_t* n_chunks, TreeState* ts, cudaStream_t st);
+void launch_derive_prefix(int level, int32_t F, int32_t B, const ull* built, const ull* prev,
+                          ull* cur, const uint8_t* small_side, cudaStream_t st);
+void launch_score(int level, int32_t F, int32_t B, const ull* cur, const int32_t* border_counts,
+                  double l2, int score_fn, double* feat_score, int32_t* feat_bin, TreeState* ts,
+                  cudaStream_t st);
+// scratch: 8 * 65536 uint32; seg_start_*: 65536 each; blk_true: ceil(n / kPartTile);
+// child_cnt: 2^(level+1) (false counts, then true counts).
+void launch_partition(int level, int64_t n, const uint8_t* bins_fm, int64_t n_stride,
+                      const uint32_t* perm, uint32_t* perm_next, uint16_t* leaf, uint32_t* seg_off,
+                      uint32_t* seg_cnt, uint32_t* scratch, uint32_t* seg_start_blk,
+                      uint32_t* seg_start_part, uint32_t* blk_true, uint32_t* child_cnt,
+                      TreeState* ts, cudaStream_t st);
+void launch_small_side(int level_next, const uint32_t* child_cnt_global, uint8_t* small_side,
+                       cudaStream_t st);
+void launch_route_leafsum(int level, int64_t n, const uint8_t* bins_fm, int64_t n_stride, uint16_t* leaf,
+                          const double* wd1, const double* weight, int depth, TreeState* ts,
+                          ull* leaf_sums, cudaStream_t st);
+void launch_leaf_values(int depth, int n_splits_expected, const ull* leaf_sums, double l2, double lr,
+                        TreeState* ts, double* leaf_raw, double* leaf_lrv, cudaStream_t st);
+void launch_leaf_export(int64_t n, const uint16_t* leaf, void* out, int bytes, cudaStream_t st);
+void launch_gradients(int64_t n, int loss, const double* approx, const double* target, double* d1,
+                      double* d2, cudaStream_t st);
+
+}  // namespace cbgpu

@@ -1,0 +1,972 @@
+// session.cu -- the C ABI (include/cbgpu.h): a B200 training session behind the
+// reference's Runtime seam (crates/cb-compute/src/runtime.rs:1410-1651).
+//
+// A session owns the quantized rows of this rank in HBM (row-major for the
+// histogram gathers, feature-major for routing), the resident approximant and
+// per-tree scratch.  grow_tree enqueues the whole tree on one stream with no
+// host synchronisation until the small result copy at the end.
+#include <cfloat>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstddef>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include <nccl.h>
+
+#include "../../include/cbgpu.h"
+#include "kernels.cuh"
+
+using namespace cbgpu;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[1024];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+#define CU(call)                                                                      \
+    do {                                                                              \
+        cudaError_t _e = (call);                                                      \
+        if (_e != cudaSuccess) {                                                      \
+            return fail(_e == cudaErrorMemoryAllocation ? CBGPU_ERR_OOM : CBGPU_ERR_CUDA, \
+                        "%s failed: %s (%s:%d)", #call, cudaGetErrorString(_e),       \
+                        __FILE__, __LINE__);                                          \
+        }                                                                             \
+    } while (0)
+
+#define NC(call)                                                                            \
+    do {                                                                                    \
+        ncclResult_t _r = (call);                                                           \
+        if (_r != ncclSuccess)                                                              \
+            return fail(CBGPU_ERR_NCCL, "%s failed: %s", #call, ncclGetErrorString(_r));    \
+    } while (0)
+
+// Host replica of the reference's main TFastRng64 stream (rng.rs), with the
+// call counter that cb-train's draw accounting is expressed in.
+struct HostRng {
+    Rng64 r{};
+    uint64_t calls = 0;
+    void seed(uint64_t s) {
+        r = Rng64::from_seed(s);
+        calls = 0;
+    }
+    uint64_t gen() {
+        ++calls;
+        return r.gen();
+    }
+    double real1() { return (double)(gen() >> 11) * (1.0 / 9007199254740991.0); }
+    void advance(uint64_t d) {
+        r.advance(d);
+        calls += d;
+    }
+    double std_normal() {  // normal.rs (Marsaglia polar)
+        for (;;) {
+            double x = real1() * 2.0 - 1.0;
+            double y = real1() * 2.0 - 1.0;
+            double rr = x * x + y * y;
+            if (!(rr > 1.0 || rr <= 0.0)) return x * std::sqrt(-2.0 * std::log(rr) / rr);
+        }
+    }
+};
+
+inline int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
+
+template <typename T>
+int dalloc(T** p, size_t count) {
+    *p = nullptr;
+    if (count == 0) count = 1;
+    cudaError_t e = cudaMalloc((void**)p, sizeof(T) * count);
+    if (e != cudaSuccess)
+        return fail(e == cudaErrorMemoryAllocation ? CBGPU_ERR_OOM : CBGPU_ERR_CUDA,
+                    "cudaMalloc(%zu bytes) failed: %s", sizeof(T) * count, cudaGetErrorString(e));
+    return CBGPU_OK;
+}
+
+#define DA(p, count)                       \
+    do {                                   \
+        int _rc = dalloc(&(p), (count));   \
+        if (_rc) return _rc;               \
+    } while (0)
+
+}  // namespace
+
+struct cbgpu_session {
+    // configuration
+    int device = 0;
+    int loss = 0, depth = 0, score_fn = 0, boot = 0, sample_from_host = 0;
+    float sample_rate = 1.0f, temp = 1.0f;
+    int has_mvs_lambda = 0;
+    double mvs_lambda = 0.0;
+    double lr = 0.0, l2 = 0.0, bias = 0.0;
+    uint64_t seed = 0;
+    int64_t n = 0, n_total = 0, row_offset = 0, n_stride = 0;
+    int F = 0, F_pad = 0, B = 0;
+    int rank = 0, world = 1;
+    bool weighted = false;
+    std::vector<int32_t> border_counts;
+
+    cudaStream_t st = nullptr;
+    ncclComm_t comm = nullptr;
+
+    // device data
+    uint8_t* bins_rm = nullptr;   // [n][F_pad]
+    uint8_t* bins_fm = nullptr;   // [F][n_stride]
+    int32_t* d_border_counts = nullptr;
+    double* target = nullptr;
+    double* weight = nullptr;
+    double* approx = nullptr;
+    double* wd1 = nullptr;
+    double2* stats = nullptr;
+    float* sw32 = nullptr;
+    double* sw64 = nullptr;
+    double* mvs_thr = nullptr;
+    uint16_t* leaf = nullptr;
+    uint32_t* perm[2] = {nullptr, nullptr};
+    uint32_t* seg_off = nullptr;
+    uint32_t* seg_cnt = nullptr;
+    uint32_t* part_scratch = nullptr;
+    uint32_t* seg_start_blk = nullptr;
+    uint32_t* seg_start_part = nullptr;
+    uint32_t* blk_true = nullptr;
+    uint32_t* child_cnt = nullptr;
+    uint8_t* small_side = nullptr;
+    HistChunk* chunks = nullptr;
+    uint32_t* n_chunks = nullptr;
+    ull* built = nullptr;
+    ull* hist[2] = {nullptr, nullptr};
+    double* feat_score = nullptr;
+    int32_t* feat_bin = nullptr;
+    ull* leaf_sums = nullptr;
+    double* leaf_raw = nullptr;
+    double* leaf_lrv = nullptr;
+    TreeState* ts = nullptr;
+    uint32_t* d_err = nullptr;
+    void* leaf_export = nullptr;
+    size_t built_cells = 0, hist_cells = 0;
+
+    // host state
+    HostRng rng;
+    bool target_ready = false;
+    bool pending = false;
+    bool has_prev_mean = false;
+    double prev_mean = 0.0;
+    int64_t trees = 0;
+    bool profiling = false;
+    cudaEvent_t ev[2 + 5 * 16 + 1] = {};
+    cudaEvent_t uev[4] = {};
+    double timing[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    TreeState h_ts{};
+};
+
+namespace {
+
+int check_args(const cbgpu_begin_args* a) {
+    if (!a) return fail(CBGPU_ERR_INVALID, "null begin args");
+    // Coverage gate (session.rs:1379-1633 / boosting.rs:5789-6010 analogue):
+    // anything outside the covered regime declines to the CPU grower.
+    if (a->grow_policy != CBGPU_GROW_SYMMETRIC)
+        return fail(CBGPU_DECLINED, "grow_policy %d is not SymmetricTree", a->grow_policy);
+    if (!a->boosting_type_is_plain) return fail(CBGPU_DECLINED, "Ordered boosting is not covered");
+    if (a->fold_count != 1) return fail(CBGPU_DECLINED, "fold_count %d != 1", a->fold_count);
+    if (a->loss < 0 || a->loss > 2) return fail(CBGPU_DECLINED, "loss %d not covered", a->loss);
+    if (a->score_function != CBGPU_SCORE_COSINE && a->score_function != CBGPU_SCORE_L2)
+        return fail(CBGPU_DECLINED, "score function %d not covered", a->score_function);
+    if (a->depth < 1 || a->depth > 16) return fail(CBGPU_DECLINED, "depth %d outside 1..16", a->depth);
+    if (a->n_bins < 2 || a->n_bins > 256)
+        return fail(CBGPU_DECLINED, "n_bins %d outside 2..256", a->n_bins);
+    if (a->bootstrap_type == CBGPU_BOOT_POISSON) return fail(CBGPU_DECLINED, "Poisson bootstrap not covered");
+    if (a->bootstrap_type < 0 || a->bootstrap_type > 4)
+        return fail(CBGPU_ERR_INVALID, "bad bootstrap type %d", a->bootstrap_type);
+    if (a->random_strength != 0.0) return fail(CBGPU_DECLINED, "random_strength != 0 is not covered");
+    if (a->n < 0 || a->n_features < 1) return fail(CBGPU_ERR_INVALID, "bad shape n=%lld F=%d",
+                                                   (long long)a->n, a->n_features);
+    if (a->n >= (int64_t)0xfffffff0ll) return fail(CBGPU_DECLINED, "n >= 2^32 rows per rank");
+    if (a->world_size < 1 || a->rank < 0 || a->rank >= a->world_size)
+        return fail(CBGPU_ERR_INVALID, "bad rank %d / world %d", a->rank, a->world_size);
+    if (a->world_size > 1 && !a->nccl_unique_id)
+        return fail(CBGPU_ERR_INVALID, "world_size > 1 needs nccl_unique_id");
+    if (a->bootstrap_type == CBGPU_BOOT_MVS && (a->row_offset % 8192) != 0)
+        return fail(CBGPU_ERR_INVALID, "MVS needs row_offset aligned to 8192 (got %lld)",
+                    (long long)a->row_offset);
+    return CBGPU_OK;
+}
+
+int alloc_session(cbgpu_session* s, const cbgpu_begin_args* a) {
+    s->device = a->device;
+    CU(cudaSetDevice(s->device));
+    CU(cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking));
+    s->loss = a->loss;
+    s->depth = a->depth;
+    s->score_fn = a->score_function;
+    s->boot = a->bootstrap_type;
+    s->sample_from_host = a->sample_from_host;
+    s->sample_rate = a->sample_rate;
+    s->temp = a->bagging_temperature;
+    s->has_mvs_lambda = a->has_mvs_lambda;
+    s->mvs_lambda = a->mvs_lambda;
+    s->lr = a->learning_rate;
+    s->l2 = a->scaled_l2;
+    s->bias = a->bias;
+    s->seed = a->rng_seed;
+    s->n = a->n;
+    s->n_total = a->n_total > 0 ? a->n_total : a->n;
+    s->row_offset = a->row_offset;
+    s->n_stride = round_up(s->n > 0 ? s->n : 1, 16);
+    s->F = a->n_features;
+    s->F_pad = (int)round_up(s->F, 32);
+    s->B = a->n_bins;
+    s->rank = a->rank;
+    s->world = a->world_size;
+    s->weighted = a->weight != nullptr;
+    s->rng.seed(a->rng_seed);
+
+    const int64_t n = s->n > 0 ? s->n : 1;
+    const int L = 1 << s->depth;
+    DA(s->bins_rm, (size_t)n * s->F_pad);
+    DA(s->bins_fm, (size_t)s->F * s->n_stride);
+    DA(s->d_border_counts, s->F);
+    DA(s->target, n);
+    if (s->weighted) DA(s->weight, n);
+    DA(s->approx, n);
+    DA(s->wd1, n);
+    DA(s->stats, n);
+    DA(s->sw32, n);
+    if (s->sample_from_host) DA(s->sw64, n);
+    DA(s->mvs_thr, (n + 8191) / 8192);
+    DA(s->leaf, n);
+    DA(s->perm[0], n);
+    DA(s->perm[1], n);
+    DA(s->seg_off, 1 << 16);
+    DA(s->seg_cnt, 1 << 16);
+    DA(s->part_scratch, 8u << 16);
+    DA(s->seg_start_blk, 1 << 16);
+    DA(s->seg_start_part, 1 << 16);
+    DA(s->blk_true, (n + kPartTile - 1) / kPartTile + 1);
+    DA(s->child_cnt, 1 << 17);
+    DA(s->small_side, 1 << 16);
+    const size_t max_chunks = (size_t)(n / kChunkRows) + (L / 2) + 2;
+    DA(s->chunks, max_chunks);
+    DA(s->n_chunks, 1);
+    s->built_cells = (size_t)(L / 2 > 0 ? L / 2 : 1) * s->F * s->B * 2;
+    s->hist_cells = (size_t)(L / 2 > 0 ? L / 2 : 1) * s->F * s->B * 2;
+    DA(s->built, s->built_cells);
+    DA(s->hist[0], s->hist_cells);
+    DA(s->hist[1], s->hist_cells);
+    DA(s->feat_score, s->F);
+    DA(s->feat_bin, s->F);
+    DA(s->leaf_sums, 2 * L);
+    DA(s->leaf_raw, L);
+    DA(s->leaf_lrv, L);
+    DA(s->ts, 1);
+    DA(s->d_err, 1);
+    CU(cudaMemsetAsync(s->ts, 0, sizeof(TreeState), s->st));
+    CU(cudaMemsetAsync(s->d_err, 0, sizeof(uint32_t), s->st));
+    CU(cudaMemsetAsync(s->leaf, 0, sizeof(uint16_t) * n, s->st));
+    if (s->weighted)
+        CU(cudaMemcpyAsync(s->weight, a->weight, sizeof(double) * s->n, cudaMemcpyHostToDevice, s->st));
+    // resident approximant starts at the bias (DeviceTrainConfig::bias)
+    {
+        std::vector<double> h((size_t)std::min<int64_t>(n, 1 << 20), s->bias);
+        for (int64_t off = 0; off < s->n; off += (int64_t)h.size()) {
+            int64_t c = std::min<int64_t>((int64_t)h.size(), s->n - off);
+            CU(cudaMemcpyAsync(s->approx + off, h.data(), sizeof(double) * c, cudaMemcpyHostToDevice, s->st));
+            CU(cudaStreamSynchronize(s->st));
+        }
+    }
+    for (auto& e : s->ev) CU(cudaEventCreate(&e));
+    for (auto& e : s->uev) CU(cudaEventCreate(&e));
+    if (s->world > 1) {
+        ncclUniqueId id;
+        memcpy(&id, a->nccl_unique_id, sizeof(id));
+        NC(ncclCommInitRank(&s->comm, s->world, id, s->rank));
+    }
+    return CBGPU_OK;
+}
+
+void free_session(cbgpu_session* s) {
+    if (!s) return;
+    cudaSetDevice(s->device);
+    if (s->st) cudaStreamSynchronize(s->st);
+    void* ptrs[] = {s->bins_rm, s->bins_fm, s->d_border_counts, s->target, s->weight, s->approx,
+                    s->wd1, s->stats, s->sw32, s->sw64, s->mvs_thr, s->leaf, s->perm[0], s->perm[1],
+                    s->seg_off, s->seg_cnt, s->part_scratch, s->seg_start_blk, s->seg_start_part,
+                    s->blk_true, s->child_cnt, s->small_side, s->chunks, s->n_chunks, s->built,
+                    s->hist[0], s->hist[1], s->feat_score, s->feat_bin, s->leaf_sums, s->leaf_raw,
+                    s->leaf_lrv, s->ts, s->d_err, s->leaf_export};
+    for (void* p : ptrs)
+        if (p) cudaFree(p);
+    for (auto& e : s->ev)
+        if (e) cudaEventDestroy(e);
+    for (auto& e : s->uev)
+        if (e) cudaEventDestroy(e);
+    if (s->comm) ncclCommDestroy(s->comm);
+    if (s->st) cudaStreamDestroy(s->st);
+    delete s;
+}
+
+int finish_begin(cbgpu_session* s) {
+    for (int f = 0; f < s->F; ++f)
+        if (s->border_counts[f] > s->B - 1)
+            return fail(CBGPU_ERR_INVALID, "feature %d has %d borders > n_bins - 1 = %d", f,
+                        s->border_counts[f], s->B - 1);
+    bool any = false;
+    for (int f = 0; f < s->F; ++f) any |= s->border_counts[f] > 0;
+    if (!any) return fail(CBGPU_DECLINED, "no feature has a border: nothing to split on");
+    CU(cudaMemcpyAsync(s->d_border_counts, s->border_counts.data(), sizeof(int32_t) * s->F,
+                       cudaMemcpyHostToDevice, s->st));
+    if (s->n > 0) launch_transpose_fm_to_rm(s->bins_fm, s->n, s->n_stride, s->F, s->bins_rm, s->F_pad, s->st);
+    uint32_t herr = 0;
+    CU(cudaMemcpyAsync(&herr, s->d_err, sizeof(uint32_t), cudaMemcpyDeviceToHost, s->st));
+    CU(cudaStreamSynchronize(s->st));
+    CU(cudaGetLastError());
+    if (herr & kErrBinRange) return fail(CBGPU_ERR_INVALID, "a bin index >= n_bins was passed");
+    return CBGPU_OK;
+}
+
+template <typename T>
+int allreduce(cbgpu_session* s, T* buf, size_t count, ncclDataType_t dt, ncclRedOp_t op) {
+    if (s->world <= 1 || count == 0) return CBGPU_OK;
+    NC(ncclAllReduce(buf, buf, count, dt, op, s->comm, s->st));
+    return CBGPU_OK;
+}
+
+float ev_ms(cbgpu_session* s, int a, int b) {
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, s->ev[a], s->ev[b]);
+    return ms;
+}
+
+// First-tree MVS lambda (bootstrap.rs:358-376): (sum |w*der1| / n)^2 with a
+// sequential f64 sum over all rows; the chain crosses ranks in rank order.
+int first_mvs_lambda(cbgpu_session* s, const double* approx_h, const double* target_h, double* out) {
+    std::vector<double> w;
+    if (s->weighted) {
+        w.resize((size_t)s->n);
+        CU(cudaMemcpy(w.data(), s->weight, sizeof(double) * s->n, cudaMemcpyDeviceToHost));
+    }
+    double acc = 0.0;
+    if (s->world > 1) {
+        double* d;
+        DA(d, 1);
+        if (s->rank > 0) {
+            ncclResult_t r = ncclRecv(d, 1, ncclFloat64, s->rank - 1, s->comm, s->st);
+            if (r != ncclSuccess) { cudaFree(d); return fail(CBGPU_ERR_NCCL, "ncclRecv: %s", ncclGetErrorString(r)); }
+            CU(cudaMemcpyAsync(&acc, d, sizeof(double), cudaMemcpyDeviceToHost, s->st));
+            CU(cudaStreamSynchronize(s->st));
+        }
+        for (int64_t i = 0; i < s->n; ++i) {
+            double a = approx_h ? approx_h[i] : s->bias;
+            double d1 = s->loss == 0 ? target_h[i] - a : target_h[i] - (1.0 - 1.0 / (1.0 + std::exp(a)));
+            double v = d1 * (s->weighted ? w[(size_t)i] : 1.0);
+            double dobj = std::sqrt(v * v);
+            acc += std::sqrt(dobj * dobj);
+        }
+        CU(cudaMemcpyAsync(d, &acc, sizeof(double), cudaMemcpyHostToDevice, s->st));
+        if (s->rank + 1 < s->world) NC(ncclSend(d, 1, ncclFloat64, s->rank + 1, s->comm, s->st));
+        NC(ncclBroadcast(d, d, 1, ncclFloat64, s->world - 1, s->comm, s->st));
+        CU(cudaMemcpyAsync(&acc, d, sizeof(double), cudaMemcpyDeviceToHost, s->st));
+        CU(cudaStreamSynchronize(s->st));
+        cudaFree(d);
+    } else {
+        for (int64_t i = 0; i < s->n; ++i) {
+            double a = approx_h ? approx_h[i] : s->bias;
+            double d1 = s->loss == 0 ? target_h[i] - a : target_h[i] - (1.0 - 1.0 / (1.0 + std::exp(a)));
+            double v = d1 * (s->weighted ? w[(size_t)i] : 1.0);
+            double dobj = std::sqrt(v * v);
+            acc += std::sqrt(dobj * dobj);
+        }
+    }
+    double mean = s->n_total > 0 ? acc / (double)s->n_total : 0.0;
+    *out = mean * mean;
+    return CBGPU_OK;
+}
+
+int grow(cbgpu_session* s, const double* approx_h, const double* target_h, int64_t n,
+         const double* sample, int64_t sample_len, int32_t* split_feature, int32_t* split_bin,
+         int32_t* n_splits, double* leaf_values, void* leaf_of, int32_t leaf_of_bytes) {
+    if (n != s->n) return fail(CBGPU_ERR_INVALID, "LengthMismatch: n=%lld, session has %lld",
+                               (long long)n, (long long)s->n);
+    // sample validation (session.rs:2405-2428)
+    if (sample_len != 0) {
+        if (!s->sample_from_host)
+            return fail(CBGPU_ERR_INVALID,
+                        "Degenerate: a %lld-element host bootstrap sample was passed to a session opened "
+                        "with sample_from_host = false", (long long)sample_len);
+        if (sample_len != s->n)
+            return fail(CBGPU_ERR_INVALID, "LengthMismatch: sample has %lld elements, expected %lld",
+                        (long long)sample_len, (long long)s->n);
+        if (!sample) return fail(CBGPU_ERR_INVALID, "null sample pointer");
+    } else if (s->sample_from_host) {
+        return fail(CBGPU_ERR_INVALID,
+                    "Degenerate: the session was opened with sample_from_host = true but no sample "
+                    "was passed");
+    }
+    if (!s->target_ready && !target_h) return fail(CBGPU_ERR_INVALID, "target required on the first grow");
+    if (leaf_of && leaf_of_bytes) {
+        if (leaf_of_bytes != 1 && leaf_of_bytes != 2 && leaf_of_bytes != 4)
+            return fail(CBGPU_ERR_INVALID, "leaf_of_bytes must be 1, 2 or 4");
+        if (leaf_of_bytes == 1 && s->depth > 8) return fail(CBGPU_ERR_INVALID, "u8 leaf ids need depth <= 8");
+    }
+    CU(cudaSetDevice(s->device));
+    cudaStream_t st = s->st;
+    const int D = s->depth;
+    const int L = 1 << D;
+    const bool prof = s->profiling;
+    int launches = 0;
+    // event slots: 0 tree start, 1 after derivatives, per level l: 2+5l .. 6+5l, last: 2+5D
+    auto rec = [&](int k) { if (prof || k == 0 || k == 2 + 5 * D) cudaEventRecord(s->ev[k], st); };
+
+    rec(0);
+    if (!s->target_ready) {
+        CU(cudaMemcpyAsync(s->target, target_h, sizeof(double) * s->n, cudaMemcpyHostToDevice, st));
+        s->target_ready = true;
+    }
+    if (approx_h) {
+        CU(cudaMemcpyAsync(s->approx, approx_h, sizeof(double) * s->n, cudaMemcpyHostToDevice, st));
+        s->pending = false;
+    }
+    CU(cudaMemsetAsync(s->ts, 0, sizeof(TreeState), st));
+
+    // ---- bootstrap: the host stream replica decides the draws (boosting.rs:6568-6660)
+    int s_mode = 0;
+    bool mvs = false;
+    uint64_t mvs_seed = 0;
+    double mvs_lam = 0.0;
+    if (s->sample_from_host) {
+        CU(cudaMemcpyAsync(s->sw64, sample, sizeof(double) * s->n, cudaMemcpyHostToDevice, st));
+        s_mode = 2;
+    } else if (s->boot != CBGPU_BOOT_NO) {
+        s->rng.gen();  // PRE_TREE_DRAWS = 2 (boosting.rs:59)
+        s->rng.gen();
+        if (s->boot == CBGPU_BOOT_BAYESIAN) {
+            if (s->temp != 0.0f) {
+                uint64_t rand_seed = s->rng.gen();
+                launch_bootstrap(1, s->n, s->row_offset, rand_seed, Rng64{}, 0.0, s->temp, s->sw32, st);
+                ++launches;
+                s_mode = 1;
+            }
+        } else if (s->boot == CBGPU_BOOT_BERNOULLI) {
+            if ((double)s->sample_rate < 1.0) {
+                Rng64 base = s->rng.r;
+                s->rng.advance((uint64_t)s->n_total);
+                launch_bootstrap(2, s->n, s->row_offset, 0, base, (double)s->sample_rate, 0.0f, s->sw32, st);
+                ++launches;
+                s_mode = 1;
+            }
+        } else if (s->boot == CBGPU_BOOT_MVS) {
+            if ((double)s->sample_rate < 1.0) {
+                if (s->has_mvs_lambda) mvs_lam = s->mvs_lambda;
+                else if (s->has_prev_mean) mvs_lam = s->prev_mean * s->prev_mean;
+                else {
+                    int rc = first_mvs_lambda(s, approx_h, target_h, &mvs_lam);
+                    if (rc) return rc;
+                }
+                mvs_seed = s->rng.gen();
+                mvs = true;
+                s_mode = 1;
+            }
+        }
+    }
+    launch_der(s->n, s->loss, s->approx, s->target, s->weight, s->leaf, s->pending ? s->leaf_lrv : nullptr,
+               s_mode, s->sw32, s->sw64, s->wd1, s->stats, s->ts, mvs, st);
+    ++launches;
+    s->pending = false;
+    if (mvs) {
+        launch_mvs(s->n, s->row_offset, s->wd1, mvs_lam, (double)s->sample_rate, mvs_seed, nullptr,
+                   s->mvs_thr, s->sw32, st);
+        launch_stats_from_sample(s->n, s->wd1, s->weight, s->sw32, s->stats, s->ts, st);
+        launches += 3;
+    }
+    {
+        ull* maxbits = (ull*)((char*)s->ts + offsetof(TreeState, maxbits));
+        int rc = allreduce(s, maxbits, 4, ncclUint64, ncclMax);
+        if (rc) return rc;
+    }
+    launch_scales(s->ts, s->n_total, st);
+    ++launches;
+    rec(1);
+
+    // ---- level loop
+    int cur = 0;
+    int pp = 0;  // current perm buffer
+    const size_t row_cells = (size_t)s->F * s->B * 2;
+    for (int l = 0; l < D; ++l) {
+        const int e = 2 + 5 * l;
+        const size_t built_slots = l == 0 ? 1 : (size_t)1 << (l - 1);
+        CU(cudaMemsetAsync(s->built, 0, sizeof(ull) * built_slots * row_cells, st));
+        const uint32_t max_chunks =
+            (uint32_t)(s->n / kChunkRows + (l == 0 ? 1 : (1u << (l - 1))) + 1);
+        launch_make_chunks(l, s->seg_off, s->seg_cnt, l ? s->small_side : nullptr, s->n, s->chunks,
+                           s->n_chunks, s->ts, st);
+        rec(e);
+        launch_hist(s->bins_rm, s->F_pad, s->F, s->B, s->stats, l == 0 ? nullptr : s->perm[pp], s->chunks,
+                    s->n_chunks, max_chunks, s->ts, s->built, st);
+        rec(e + 1);
+        launches += 2;
+        {
+            int rc = allreduce(s, s->built, built_slots * row_cells, ncclUint64, ncclSum);
+            if (rc) return rc;
+        }
+        rec(e + 2);
+        launch_derive_prefix(l, s->F, s->B, s->built, s->hist[cur ^ 1], s->hist[cur], s->small_side, st);
+        launch_score(l, s->F, s->B, s->hist[cur], s->d_border_counts, s->l2, s->score_fn, s->feat_score,
+                     s->feat_bin, s->ts, st);
+        launches += 2;
+        rec(e + 3);
+        if (l + 1 < D) {
+            launch_partition(l, s->n, s->bins_fm, s->n_stride, l == 0 ? nullptr : s->perm[pp],
+                             s->perm[pp ^ 1], s->leaf, s->seg_off, s->seg_cnt, s->part_scratch,
+                             s->seg_start_blk, s->seg_start_part, s->blk_true, s->child_cnt, s->ts, st);
+            pp ^= 1;
+            rec(e + 4);
+            int rc = allreduce(s, s->child_cnt, (size_t)2 << l, ncclUint32, ncclSum);
+            if (rc) return rc;
+            launch_small_side(l + 1, s->child_cnt, s->small_side, st);
+            launches += 4;
+        } else {
+            CU(cudaMemsetAsync(s->leaf_sums, 0, sizeof(ull) * 2 * L, st));
+            launch_route_leafsum(l, s->n, s->bins_fm, s->n_stride, s->leaf, s->wd1, s->weight, D, s->ts,
+                                 s->leaf_sums, st);
+            ++launches;
+            rec(e + 4);
+            int rc = allreduce(s, s->leaf_sums, (size_t)2 * L, ncclUint64, ncclSum);
+            if (rc) return rc;
+        }
+        cur ^= 1;
+    }
+    launch_leaf_values(D, D, s->leaf_sums, s->l2, s->lr, s->ts, s->leaf_raw, s->leaf_lrv, st);
+    ++launches;
+    CU(cudaGetLastError());
+    CU(cudaMemcpyAsync(&s->h_ts, s->ts, sizeof(TreeState), cudaMemcpyDeviceToHost, st));
+    std::vector<double> raw((size_t)L);
+    CU(cudaMemcpyAsync(raw.data(), s->leaf_raw, sizeof(double) * L, cudaMemcpyDeviceToHost, st));
+    if (leaf_of && leaf_of_bytes) {
+        if (!s->leaf_export) DA(*(uint32_t**)&s->leaf_export, s->n);
+        launch_leaf_export(s->n, s->leaf, s->leaf_export, leaf_of_bytes, st);
+        ++launches;
+        CU(cudaMemcpyAsync(leaf_of, s->leaf_export, (size_t)leaf_of_bytes * s->n, cudaMemcpyDeviceToHost, st));
+    }
+    rec(2 + 5 * D);
+    CU(cudaStreamSynchronize(st));
+    CU(cudaGetLastError());
+    if (s->h_ts.err) {
+        if (s->h_ts.err & kErrNoCandidate)
+            return fail(CBGPU_ERR_DEVICE, "Degenerate: no split candidate available");
+        return fail(CBGPU_ERR_DEVICE, "device error word 0x%x (non-finite derivative or range error)",
+                    s->h_ts.err);
+    }
+    for (int l = 0; l < D; ++l) {
+        if (split_feature) split_feature[l] = s->h_ts.split[l].feature;
+        if (split_bin) split_bin[l] = s->h_ts.split[l].bin;
+    }
+    if (n_splits) *n_splits = D;
+    if (leaf_values) memcpy(leaf_values, raw.data(), sizeof(double) * L);
+    s->pending = true;
+    // RNG phase after the tree (boosting.rs:7267-7300 + device_draw_replay.rs)
+    if (!s->sample_from_host && s->boot != CBGPU_BOOT_NO) {
+        for (int l = 0; l < D; ++l) {
+            for (int f = 0; f < s->F; ++f) (void)s->rng.real1();
+            (void)s->rng.gen();
+            for (int f = 0; f < s->F; ++f) (void)s->rng.std_normal();
+        }
+        s->rng.gen();  // POST_TREE_EXTRA_DRAWS = 2
+        s->rng.gen();
+    }
+    // last_iter_mean_leaf_value over the learning-rate-scaled leaves (bootstrap.rs:382-389)
+    double acc = 0.0;
+    for (int k = 0; k < L; ++k) {
+        double v = raw[(size_t)k] * s->lr;
+        acc += std::sqrt(v * v);
+    }
+    s->prev_mean = acc / (double)L;
+    s->has_prev_mean = true;
+    s->trees++;
+    // timing
+    s->timing[0] = ev_ms(s, 0, 2 + 5 * D);
+    double rows = 0;
+    for (int l = 0; l < D; ++l) rows += (double)s->h_ts.hist_rows[l];
+    s->timing[6] = rows;
+    s->timing[7] = (double)launches;
+    if (prof) {
+        double th = 0, tsc = 0, tp = 0, tc = 0;
+        for (int l = 0; l < D; ++l) {
+            const int e = 2 + 5 * l;
+            th += ev_ms(s, e, e + 1);
+            tc += ev_ms(s, e + 1, e + 2);
+            tsc += ev_ms(s, e + 2, e + 3);
+            tp += ev_ms(s, e + 3, e + 4);
+        }
+        s->timing[1] = th;
+        s->timing[2] = tsc;
+        s->timing[3] = tp;
+        s->timing[4] = ev_ms(s, 0, 1);
+        s->timing[5] = tc;
+    }
+    return CBGPU_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* cbgpu_last_error(void) { return g_last_error.c_str(); }
+
+const char* cbgpu_version(void) { return "cbgpu 0.1.0 (sm_100a)"; }
+
+int cbgpu_nccl_unique_id(uint8_t* out128) {
+    if (!out128) return fail(CBGPU_ERR_INVALID, "null output");
+    ncclUniqueId id;
+    NC(ncclGetUniqueId(&id));
+    static_assert(sizeof(id) == 128, "ncclUniqueId is 128 bytes");
+    memcpy(out128, &id, sizeof(id));
+    return CBGPU_OK;
+}
+
+int cbgpu_begin(const cbgpu_begin_args* a, const uint32_t* bins_feature_major, cbgpu_session** out) {
+    if (!out) return fail(CBGPU_ERR_INVALID, "null out");
+    *out = nullptr;
+    int rc = check_args(a);
+    if (rc) return rc;
+    if (!bins_feature_major && a->n > 0) return fail(CBGPU_ERR_INVALID, "null bins");
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0)
+        return fail(CBGPU_ERR_NO_DEVICE, "no CUDA device");
+    cbgpu_session* s = new cbgpu_session();
+    rc = alloc_session(s, a);
+    if (rc) { free_session(s); return rc; }
+    s->border_counts.assign((size_t)s->F, s->B - 1);
+    if (a->border_counts)
+        for (int f = 0; f < s->F; ++f) s->border_counts[(size_t)f] = a->border_counts[f];
+    // per-feature column upload + range-checked narrowing to u8
+    uint32_t* tmp = nullptr;
+    if (s->n > 0) {
+        rc = dalloc(&tmp, (size_t)s->n);
+        if (rc) { free_session(s); return rc; }
+        for (int f = 0; f < s->F && !rc; ++f) {
+            cudaError_t e = cudaMemcpyAsync(tmp, bins_feature_major + (size_t)f * s->n,
+                                            sizeof(uint32_t) * s->n, cudaMemcpyHostToDevice, s->st);
+            if (e != cudaSuccess) rc = fail(CBGPU_ERR_CUDA, "bins upload: %s", cudaGetErrorString(e));
+            launch_u32_to_u8_column(tmp, s->n, s->B, s->bins_fm + (size_t)f * s->n_stride, s->d_err, s->st);
+        }
+        cudaStreamSynchronize(s->st);
+        cudaFree(tmp);
+    }
+    if (!rc) rc = finish_begin(s);
+    if (rc) { free_session(s); return rc; }
+    *out = s;
+    return CBGPU_OK;
+}
+
+int cbgpu_begin_raw(const cbgpu_begin_args* a, const float* const* cols, const double* borders_flat,
+                    const int32_t* border_counts, cbgpu_session** out) {
+    if (!out) return fail(CBGPU_ERR_INVALID, "null out");
+    *out = nullptr;
+    int rc = check_args(a);
+    if (rc) return rc;
+    if (!border_counts || (!cols && a->n > 0)) return fail(CBGPU_ERR_INVALID, "null columns / borders");
+    int maxb = 0;
+    int64_t off = 0;
+    for (int f = 0; f < a->n_features; ++f) {
+        if (border_counts[f] < 0 || border_counts[f] > 255)
+            return fail(CBGPU_DECLINED, "feature %d has %d borders (> 255)", f, border_counts[f]);
+        for (int k = 1; k < border_counts[f]; ++k)
+            if (!(borders_flat[off + k - 1] <= borders_flat[off + k]))
+                return fail(CBGPU_ERR_INVALID, "feature %d borders are not ascending", f);
+        off += border_counts[f];
+        maxb = std::max(maxb, border_counts[f]);
+    }
+    if (maxb + 1 > a->n_bins) return fail(CBGPU_ERR_INVALID, "n_bins %d < max borders + 1 = %d", a->n_bins, maxb + 1);
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0)
+        return fail(CBGPU_ERR_NO_DEVICE, "no CUDA device");
+    cbgpu_session* s = new cbgpu_session();
+    rc = alloc_session(s, a);
+    if (rc) { free_session(s); return rc; }
+    s->border_counts.assign(border_counts, border_counts + a->n_features);
+    float* col = nullptr;
+    double* bord = nullptr;
+    if (s->n > 0) {
+        rc = dalloc(&col, (size_t)s->n);
+        if (!rc) rc = dalloc(&bord, (size_t)(off > 0 ? off : 1));
+        if (!rc && off > 0) {
+            cudaError_t e = cudaMemcpy(bord, borders_flat, sizeof(double) * off, cudaMemcpyHostToDevice);
+            if (e != cudaSuccess) rc = fail(CBGPU_ERR_CUDA, "borders upload: %s", cudaGetErrorString(e));
+        }
+        int64_t boff = 0;
+        for (int f = 0; f < s->F && !rc; ++f) {
+            cudaError_t e = cudaMemcpyAsync(col, cols[f], sizeof(float) * s->n, cudaMemcpyHostToDevice, s->st);
+            if (e != cudaSuccess) rc = fail(CBGPU_ERR_CUDA, "column upload: %s", cudaGetErrorString(e));
+            launch_quantize_column(col, s->n, bord + boff, border_counts[f],
+                                   s->bins_fm + (size_t)f * s->n_stride, s->d_err, s->st);
+            boff += border_counts[f];
+        }
+        cudaStreamSynchronize(s->st);
+        if (col) cudaFree(col);
+        if (bord) cudaFree(bord);
+    }
+    if (!rc) rc = finish_begin(s);
+    if (rc) { free_session(s); return rc; }
+    *out = s;
+    return CBGPU_OK;
+}
+
+int cbgpu_grow_tree(cbgpu_session* s, const double* approx, const double* target, int64_t n,
+                    const double* sample, int64_t sample_len, int32_t* split_feature, int32_t* split_bin,
+                    int32_t* n_splits, double* leaf_values, void* leaf_of, int32_t leaf_of_bytes) {
+    if (!s) return fail(CBGPU_ERR_INVALID, "null session");
+    return grow(s, approx, target, n, sample, sample_len, split_feature, split_bin, n_splits,
+                leaf_values, leaf_of, leaf_of_bytes);
+}
+
+int cbgpu_end(cbgpu_session* s) {
+    free_session(s);
+    return CBGPU_OK;
+}
+
+int cbgpu_session_approx(cbgpu_session* s, double* out, int64_t n) {
+    if (!s || !out || n != s->n) return fail(CBGPU_ERR_INVALID, "bad arguments");
+    CU(cudaSetDevice(s->device));
+    if (s->pending) {
+        launch_apply(s->n, s->approx, s->leaf, s->leaf_lrv, s->st);
+        s->pending = false;
+    }
+    CU(cudaMemcpyAsync(out, s->approx, sizeof(double) * n, cudaMemcpyDeviceToHost, s->st));
+    CU(cudaStreamSynchronize(s->st));
+    return CBGPU_OK;
+}
+
+int cbgpu_session_bins(cbgpu_session* s, uint8_t* out, int64_t n, int32_t F) {
+    if (!s || !out || n != s->n || F != s->F) return fail(CBGPU_ERR_INVALID, "bad arguments");
+    CU(cudaSetDevice(s->device));
+    for (int f = 0; f < F; ++f)
+        CU(cudaMemcpyAsync(out + (size_t)f * n, s->bins_fm + (size_t)f * s->n_stride, n,
+                           cudaMemcpyDeviceToHost, s->st));
+    CU(cudaStreamSynchronize(s->st));
+    return CBGPU_OK;
+}
+
+int cbgpu_session_last_sample(cbgpu_session* s, double* out, int64_t n) {
+    if (!s || !out || n != s->n) return fail(CBGPU_ERR_INVALID, "bad arguments");
+    CU(cudaSetDevice(s->device));
+    std::vector<double2> st((size_t)n);
+    std::vector<double> wd((size_t)n);
+    CU(cudaMemcpy(st.data(), s->stats, sizeof(double2) * n, cudaMemcpyDeviceToHost));
+    if (s->sample_from_host) {
+        CU(cudaMemcpy(out, s->sw64, sizeof(double) * n, cudaMemcpyDeviceToHost));
+        return CBGPU_OK;
+    }
+    std::vector<float> sw((size_t)n);
+    CU(cudaMemcpy(sw.data(), s->sw32, sizeof(float) * n, cudaMemcpyDeviceToHost));
+    for (int64_t i = 0; i < n; ++i) out[i] = (double)sw[(size_t)i];
+    return CBGPU_OK;
+}
+
+int cbgpu_session_timing(cbgpu_session* s, double* out8) {
+    if (!s || !out8) return fail(CBGPU_ERR_INVALID, "bad arguments");
+    for (int k = 0; k < 8; ++k) out8[k] = s->timing[k];
+    return CBGPU_OK;
+}
+
+int cbgpu_session_mark(cbgpu_session* s, int32_t slot) {
+    if (!s || slot < 0 || slot > 3) return fail(CBGPU_ERR_INVALID, "bad arguments");
+    CU(cudaSetDevice(s->device));
+    CU(cudaEventRecord(s->uev[slot], s->st));
+    return CBGPU_OK;
+}
+
+int cbgpu_session_elapsed_ms(cbgpu_session* s, int32_t a, int32_t b, double* out) {
+    if (!s || !out || a < 0 || a > 3 || b < 0 || b > 3) return fail(CBGPU_ERR_INVALID, "bad arguments");
+    CU(cudaSetDevice(s->device));
+    CU(cudaEventSynchronize(s->uev[b]));
+    float ms = 0.f;
+    CU(cudaEventElapsedTime(&ms, s->uev[a], s->uev[b]));
+    *out = ms;
+    return CBGPU_OK;
+}
+
+int cbgpu_session_set_profiling(cbgpu_session* s, int32_t enabled) {
+    if (!s) return fail(CBGPU_ERR_INVALID, "null session");
+    s->profiling = enabled != 0;
+    return CBGPU_OK;
+}
+
+int cbgpu_session_rng_state(cbgpu_session* s, uint64_t* out5) {
+    if (!s || !out5) return fail(CBGPU_ERR_INVALID, "bad arguments");
+    out5[0] = s->rng.r.x1;
+    out5[1] = s->rng.r.c1;
+    out5[2] = s->rng.r.x2;
+    out5[3] = s->rng.r.c2;
+    out5[4] = s->rng.calls;
+    return CBGPU_OK;
+}
+
+int cbgpu_compute_gradients(int32_t loss, const double* approx, const double* target, int64_t n,
+                            double* der1, double* der2) {
+    if (loss < 0 || loss > 2) return fail(CBGPU_DECLINED, "loss %d not covered", loss);
+    if (n < 0 || (n > 0 && (!approx || !target || !der1)))
+        return fail(CBGPU_ERR_INVALID, "bad arguments");
+    if (n == 0) return CBGPU_OK;
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0)
+        return fail(CBGPU_ERR_NO_DEVICE, "no CUDA device");
+    double *a, *t, *d1, *d2 = nullptr;
+    DA(a, n);
+    DA(t, n);
+    DA(d1, n);
+    if (der2) DA(d2, n);
+    CU(cudaMemcpy(a, approx, sizeof(double) * n, cudaMemcpyHostToDevice));
+    CU(cudaMemcpy(t, target, sizeof(double) * n, cudaMemcpyHostToDevice));
+    launch_gradients(n, loss, a, t, d1, d2, 0);
+    CU(cudaMemcpy(der1, d1, sizeof(double) * n, cudaMemcpyDeviceToHost));
+    if (der2) CU(cudaMemcpy(der2, d2, sizeof(double) * n, cudaMemcpyDeviceToHost));
+    cudaFree(a);
+    cudaFree(t);
+    cudaFree(d1);
+    if (d2) cudaFree(d2);
+    return CBGPU_OK;
+}
+
+int cbgpu_histogram(const uint8_t* bins_rm_h, int64_t n, int32_t F, int32_t B, const double* g,
+                    const double* h, const int32_t* leaf_of, int32_t n_leaves, double* out_hist) {
+    if (n < 0 || F < 1 || B < 1 || B > 256 || n_leaves < 1 || !out_hist || (n > 0 && (!bins_rm_h || !g || !h)))
+        return fail(CBGPU_ERR_INVALID, "bad arguments");
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0)
+        return fail(CBGPU_ERR_NO_DEVICE, "no CUDA device");
+    const int F_pad = (int)round_up(F, 32);
+    // host: stable counting sort of rows by leaf -> one contiguous segment per leaf
+    std::vector<uint32_t> perm;
+    std::vector<HistChunk> chunks;
+    perm.reserve((size_t)n);
+    {
+        std::vector<int64_t> cnt((size_t)n_leaves + 1, 0);
+        for (int64_t i = 0; i < n; ++i) {
+            int32_t q = leaf_of ? leaf_of[i] : 0;
+            if (q >= 0 && q < n_leaves) cnt[(size_t)q + 1]++;
+        }
+        for (int q = 0; q < n_leaves; ++q) cnt[(size_t)q + 1] += cnt[(size_t)q];
+        perm.resize((size_t)cnt[(size_t)n_leaves]);
+        std::vector<int64_t> pos(cnt.begin(), cnt.end() - 1);
+        for (int64_t i = 0; i < n; ++i) {
+            int32_t q = leaf_of ? leaf_of[i] : 0;
+            if (q >= 0 && q < n_leaves) perm[(size_t)pos[(size_t)q]++] = (uint32_t)i;
+        }
+        for (int q = 0; q < n_leaves; ++q)
+            for (int64_t st0 = cnt[(size_t)q]; st0 < cnt[(size_t)q + 1]; st0 += kChunkRows)
+                chunks.push_back(HistChunk{(uint32_t)q, (uint32_t)st0,
+                                           (uint32_t)std::min<int64_t>(kChunkRows, cnt[(size_t)q + 1] - st0), 0u});
+    }
+    std::vector<uint8_t> rm((size_t)std::max<int64_t>(n, 1) * F_pad, 0);
+    for (int64_t i = 0; i < n; ++i) memcpy(&rm[(size_t)i * F_pad], bins_rm_h + (size_t)i * F, (size_t)F);
+    // the scales: max |g|, |h| over the rows, as the session derives them
+    double mg = 0.0, mh = 0.0;
+    for (int64_t i = 0; i < n; ++i) {
+        mg = std::max(mg, std::fabs(g[i]));
+        mh = std::max(mh, std::fabs(h[i]));
+    }
+    TreeState hts{};
+    double mx[2] = {mg, mh};
+    for (int c = 0; c < 2; ++c) {
+        int s = 0;
+        if (mx[c] > 0.0) {
+            int e;
+            std::frexp(mx[c] * (double)std::max<int64_t>(n, 1), &e);
+            s = 62 - e;
+        }
+        hts.sc.scale[c] = std::ldexp(1.0, s);
+        hts.sc.inv[c] = std::ldexp(1.0, -s);
+    }
+    uint8_t* d_rm;
+    double2* d_st;
+    uint32_t *d_perm, *d_nch;
+    HistChunk* d_ch;
+    TreeState* d_ts;
+    ull* d_out;
+    const size_t cells = (size_t)n_leaves * F * B * 2;
+    DA(d_rm, rm.size());
+    DA(d_st, (size_t)std::max<int64_t>(n, 1));
+    DA(d_perm, std::max<size_t>(perm.size(), 1));
+    DA(d_ch, std::max<size_t>(chunks.size(), 1));
+    DA(d_nch, 1);
+    DA(d_ts, 1);
+    DA(d_out, cells);
+    std::vector<double2> st((size_t)n);
+    for (int64_t i = 0; i < n; ++i) st[(size_t)i] = make_double2(g[i], h[i]);
+    uint32_t nch = (uint32_t)chunks.size();
+    CU(cudaMemcpy(d_rm, rm.data(), rm.size(), cudaMemcpyHostToDevice));
+    if (n > 0) CU(cudaMemcpy(d_st, st.data(), sizeof(double2) * n, cudaMemcpyHostToDevice));
+    if (!perm.empty()) CU(cudaMemcpy(d_perm, perm.data(), sizeof(uint32_t) * perm.size(), cudaMemcpyHostToDevice));
+    if (!chunks.empty()) CU(cudaMemcpy(d_ch, chunks.data(), sizeof(HistChunk) * chunks.size(), cudaMemcpyHostToDevice));
+    CU(cudaMemcpy(d_nch, &nch, sizeof(uint32_t), cudaMemcpyHostToDevice));
+    CU(cudaMemcpy(d_ts, &hts, sizeof(TreeState), cudaMemcpyHostToDevice));
+    CU(cudaMemset(d_out, 0, sizeof(ull) * cells));
+    // bin range check on the host (the device kernel trusts its inputs)
+    for (int64_t i = 0; i < n; ++i)
+        for (int f = 0; f < F; ++f)
+            if (bins_rm_h[(size_t)i * F + f] >= B) {
+                cudaFree(d_rm); cudaFree(d_st); cudaFree(d_perm); cudaFree(d_ch); cudaFree(d_nch);
+                cudaFree(d_ts); cudaFree(d_out);
+                return fail(CBGPU_ERR_INVALID, "bin %d >= n_bins %d at row %lld feature %d",
+                            bins_rm_h[(size_t)i * F + f], B, (long long)i, f);
+            }
+    launch_hist(d_rm, F_pad, F, B, d_st, d_perm, d_ch, d_nch, std::max<uint32_t>(nch, 1), d_ts, d_out, 0);
+    CU(cudaGetLastError());
+    std::vector<ull> hout(cells);
+    CU(cudaMemcpy(hout.data(), d_out, sizeof(ull) * cells, cudaMemcpyDeviceToHost));
+    for (size_t k = 0; k < cells; ++k)
+        out_hist[k] = (double)(long long)hout[k] * hts.sc.inv[k & 1];
+    cudaFree(d_rm); cudaFree(d_st); cudaFree(d_perm); cudaFree(d_ch); cudaFree(d_nch);
+    cudaFree(d_ts); cudaFree(d_out);
+    return CBGPU_OK;
+}
+
+int cbgpu_bootstrap_weights(int32_t type, int64_t n, int64_t row_offset, uint64_t rand_seed,
+                            const uint64_t* rng_raw4, float sample_rate, float temp,
+                            const double* der_obj, double lambda, double* out) {
+    if (n < 0 || (n > 0 && !out)) return fail(CBGPU_ERR_INVALID, "bad arguments");
+    if (n == 0) return CBGPU_OK;
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0)
+        return fail(CBGPU_ERR_NO_DEVICE, "no CUDA device");
+    float* d_sw;
+    DA(d_sw, n);
+    double* d_der = nullptr;
+    double* d_thr = nullptr;
+    if (type == CBGPU_BOOT_BAYESIAN) {
+        launch_bootstrap(1, n, row_offset, rand_seed, Rng64{}, 0.0, temp, d_sw, 0);
+    } else if (type == CBGPU_BOOT_BERNOULLI) {
+        if (!rng_raw4) { cudaFree(d_sw); return fail(CBGPU_ERR_INVALID, "Bernoulli needs rng_raw4"); }
+        Rng64 base{rng_raw4[0], rng_raw4[1], rng_raw4[2], rng_raw4[3]};
+        launch_bootstrap(2, n, row_offset, 0, base, (double)sample_rate, 0.0f, d_sw, 0);
+    } else if (type == CBGPU_BOOT_MVS) {
+        if (!der_obj || row_offset % 8192) { cudaFree(d_sw); return fail(CBGPU_ERR_INVALID, "MVS needs der_obj, aligned row_offset"); }
+        DA(d_der, n);
+        DA(d_thr, (n + 8191) / 8192);
+        CU(cudaMemcpy(d_der, der_obj, sizeof(double) * n, cudaMemcpyHostToDevice));
+        launch_mvs(n, row_offset, d_der, lambda, (double)sample_rate, rand_seed, nullptr, d_thr, d_sw, 0);
+    } else {
+        cudaFree(d_sw);
+        return fail(CBGPU_ERR_INVALID, "bootstrap type %d has no device weights", type);
+    }
+    CU(cudaGetLastError());
+    std::vector<float> h((size_t)n);
+    CU(cudaMemcpy(h.data(), d_sw, sizeof(float) * n, cudaMemcpyDeviceToHost));
+    for (int64_t i = 0; i < n; ++i) out[i] = (double)h[(size_t)i];
+    cudaFree(d_sw);
+    if (d_der) cudaFree(d_der);
+    if (d_thr) cudaFree(d_thr);
+    return CBGPU_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,296 @@
+"""Host-side mirror of the reference's device seam, `cb_compute::Runtime`
+(crates/cb-compute/src/runtime.rs:1410-1651), backed by libcbgpu.so.
+
+Method names, argument meaning and decline/error behaviour follow the trait:
+begin_* returns False when the session declines (the trait's Ok(false)),
+grow_tree_on_device returns None when no session is open (Ok(None)), and
+invalid input raises CbGpuError (the CbError analogue: LengthMismatch /
+Degenerate).  The types mirror DeviceTrainConfig (runtime.rs:1259-1372) and
+DeviceGrownTree (runtime.rs:989-1059).
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass, field
+from typing import Optional, Sequence
+
+import numpy as np
+
+from . import _lib
+
+LOSS = {"RMSE": 0, "Rmse": 0, "Logloss": 1, "CrossEntropy": 2}
+SCORE = {"Cosine": 0, "L2": 1, "SolarL2": 2, "NewtonL2": 3, "NewtonCosine": 4, "LOOL2": 5, "SatL2": 6}
+BOOT = {"No": 0, "Bayesian": 1, "Bernoulli": 2, "MVS": 3, "Mvs": 3, "Poisson": 4}
+GROW = {"SymmetricTree": 0, "Depthwise": 1, "Lossguide": 2, "Region": 3}
+
+
+@dataclass
+class DeviceTrainConfig:
+    """DeviceTrainConfig (runtime.rs:1259-1372) plus this build's placement fields."""
+    grow_policy: str = "SymmetricTree"
+    bootstrap_type: str = "No"
+    sample_rate: float = 1.0
+    mvs_lambda: Optional[float] = None
+    rng_seed: int = 0
+    bias: float = 0.0
+    sample_from_host: bool = False
+    bagging_temperature: float = 1.0
+    random_strength: float = 0.0
+    border_counts: Optional[Sequence[int]] = None
+    # document sharding (one process per GPU)
+    device: int = 0
+    rank: int = 0
+    world_size: int = 1
+    row_offset: int = 0
+    n_total: Optional[int] = None
+    nccl_unique_id: Optional[bytes] = None
+
+
+@dataclass
+class Derivatives:
+    der1: np.ndarray
+    der2: np.ndarray
+
+
+@dataclass
+class DeviceGrownTree:
+    """DeviceGrownTree (runtime.rs:989-1059) for the oblivious arm."""
+    splits: list                  # [(feature, bin_id, is_one_hot)] in level order (bit l = split l)
+    leaf_values: np.ndarray       # 2^depth raw deltas, NOT scaled by learning_rate
+    approx_dim: int = 1
+    leaf_of: np.ndarray = field(default_factory=lambda: np.zeros(0, dtype=np.uint32))
+    step_nodes: list = field(default_factory=list)
+    node_id_to_leaf_id: list = field(default_factory=list)
+    region_path: list = field(default_factory=list)
+
+
+def _ptr(a):
+    return None if a is None else a.ctypes.data
+
+
+def nccl_unique_id() -> bytes:
+    L = _lib.load()
+    buf = (C.c_uint8 * 128)()
+    _lib.check(L.cbgpu_nccl_unique_id(buf))
+    return bytes(buf)
+
+
+class B200Runtime:
+    """`impl Runtime` for the B200 backend (one session per fit)."""
+
+    def __init__(self):
+        self._L = _lib.load()
+        self._s = C.c_void_p(None)
+        self.n = 0
+        self.depth = 0
+        self.decline_reason = ""
+        self._keep = []
+
+    # ---- Runtime::compute_gradients (runtime.rs:1431) -----------------------
+    def compute_gradients(self, loss, approx, target, approx_dimension: int = 1) -> Derivatives:
+        if approx_dimension != 1:
+            raise _lib.CbGpuError(_lib.DECLINED, "approx_dimension != 1 is not covered")
+        a = np.ascontiguousarray(approx, dtype=np.float64)
+        t = np.ascontiguousarray(target, dtype=np.float64)
+        if a.shape != t.shape:
+            raise _lib.CbGpuError(_lib.ERR_INVALID, "LengthMismatch: approx vs target")
+        d1, d2 = np.empty_like(a), np.empty_like(a)
+        rc = self._L.cbgpu_compute_gradients(LOSS[loss], _ptr(a), _ptr(t), a.size, _ptr(d1), _ptr(d2))
+        if rc == _lib.DECLINED:
+            raise _lib.CbGpuError(rc, _lib.last_error())
+        _lib.check(rc)
+        return Derivatives(d1, d2)
+
+    # ---- begin -------------------------------------------------------------
+    def _args(self, loss, depth, plain, fold_count, score_function, weight, n, n_features, n_bins,
+              learning_rate, scaled_l2, cfg: DeviceTrainConfig):
+        w = None if weight is None or len(weight) == 0 else np.ascontiguousarray(weight, dtype=np.float64)
+        if w is not None and w.size != n:
+            raise _lib.CbGpuError(_lib.ERR_INVALID, f"LengthMismatch: weight has {w.size}, expected {n}")
+        bc = None if cfg.border_counts is None else np.ascontiguousarray(cfg.border_counts, dtype=np.int32)
+        uid = None
+        if cfg.world_size > 1:
+            if cfg.nccl_unique_id is None or len(cfg.nccl_unique_id) != 128:
+                raise _lib.CbGpuError(_lib.ERR_INVALID, "world_size > 1 needs a 128-byte nccl_unique_id")
+            uid = np.frombuffer(cfg.nccl_unique_id, dtype=np.uint8).copy()
+        self._keep = [w, bc, uid]
+        a = _lib.BeginArgs()
+        a.loss = LOSS[loss]
+        a.depth = depth
+        a.boosting_type_is_plain = 1 if plain else 0
+        a.fold_count = fold_count
+        a.score_function = SCORE[score_function]
+        a.n = n
+        a.n_features = n_features
+        a.n_bins = n_bins
+        a.learning_rate = learning_rate
+        a.scaled_l2 = scaled_l2
+        a.weight = _ptr(w)
+        a.grow_policy = GROW[cfg.grow_policy]
+        a.bootstrap_type = BOOT[cfg.bootstrap_type]
+        a.sample_rate = cfg.sample_rate
+        a.bagging_temperature = cfg.bagging_temperature
+        a.has_mvs_lambda = 0 if cfg.mvs_lambda is None else 1
+        a.mvs_lambda = 0.0 if cfg.mvs_lambda is None else cfg.mvs_lambda
+        a.rng_seed = cfg.rng_seed & (2**64 - 1)
+        a.bias = cfg.bias
+        a.sample_from_host = 1 if cfg.sample_from_host else 0
+        a.random_strength = cfg.random_strength
+        a.device = cfg.device
+        a.rank = cfg.rank
+        a.world_size = cfg.world_size
+        a.row_offset = cfg.row_offset
+        a.n_total = cfg.n_total if cfg.n_total is not None else n
+        a.nccl_unique_id = _ptr(uid)
+        a.border_counts = _ptr(bc)
+        return a
+
+    def _finish_begin(self, rc, n, depth) -> bool:
+        if rc == _lib.DECLINED:
+            self.decline_reason = _lib.last_error()
+            self._s = C.c_void_p(None)
+            return False
+        _lib.check(rc)
+        self.n, self.depth = n, depth
+        return True
+
+    def begin_device_training(self, loss, depth, boosting_type_is_plain, fold_count, score_function,
+                              bins_feature_major, weight, n, n_features, n_bins, learning_rate,
+                              scaled_l2, config: DeviceTrainConfig) -> bool:
+        """Runtime::begin_device_training (runtime.rs:1497): u32 feature-major bins."""
+        self.end_device_training()
+        bins = np.ascontiguousarray(bins_feature_major, dtype=np.uint32).reshape(-1)
+        if bins.size != n * n_features:
+            raise _lib.CbGpuError(_lib.ERR_INVALID, "LengthMismatch: bins_feature_major")
+        a = self._args(loss, depth, boosting_type_is_plain, fold_count, score_function, weight, n,
+                       n_features, n_bins, learning_rate, scaled_l2, config)
+        rc = self._L.cbgpu_begin(C.byref(a), _ptr(bins), C.byref(self._s))
+        return self._finish_begin(rc, n, depth)
+
+    def begin_device_training_raw(self, loss, depth, boosting_type_is_plain, fold_count, score_function,
+                                  float_columns, feature_borders, weight, n, n_features, n_bins,
+                                  learning_rate, scaled_l2, config: DeviceTrainConfig) -> bool:
+        """Runtime::begin_device_training_raw (runtime.rs:1546): device quantization."""
+        self.end_device_training()
+        cols = [np.ascontiguousarray(c, dtype=np.float32) for c in float_columns]
+        if len(cols) != n_features or any(c.size != n for c in cols):
+            raise _lib.CbGpuError(_lib.ERR_INVALID, "LengthMismatch: float_columns")
+        counts = np.array([len(b) for b in feature_borders], dtype=np.int32)
+        flat = np.ascontiguousarray(
+            np.concatenate([np.asarray(b, dtype=np.float64) for b in feature_borders])
+            if counts.sum() else np.zeros(1), dtype=np.float64)
+        colptrs = (C.c_void_p * max(1, len(cols)))(*[c.ctypes.data for c in cols])
+        a = self._args(loss, depth, boosting_type_is_plain, fold_count, score_function, weight, n,
+                       n_features, n_bins, learning_rate, scaled_l2, config)
+        rc = self._L.cbgpu_begin_raw(C.byref(a), colptrs, _ptr(flat), _ptr(counts), C.byref(self._s))
+        return self._finish_begin(rc, n, depth)
+
+    # ---- Runtime::grow_tree_on_device (runtime.rs:1629) ---------------------
+    def grow_tree_on_device(self, approx, target, sample, family=None, leaf_of_bytes: int = 4,
+                            resident_approx: bool = False) -> Optional[DeviceGrownTree]:
+        if not self._s:
+            return None
+        if family is not None:
+            raise _lib.CbGpuError(_lib.DECLINED, "family trees (ranking/pairwise/multi-output) are not covered")
+        a = None if resident_approx or approx is None else np.ascontiguousarray(approx, dtype=np.float64)
+        t = None if target is None else np.ascontiguousarray(target, dtype=np.float64)
+        s = None if sample is None or len(sample) == 0 else np.ascontiguousarray(sample, dtype=np.float64)
+        if a is not None and a.size != self.n:
+            raise _lib.CbGpuError(_lib.ERR_INVALID, f"LengthMismatch: approx has {a.size}, expected {self.n}")
+        if t is not None and t.size != self.n:
+            raise _lib.CbGpuError(_lib.ERR_INVALID, f"LengthMismatch: target has {t.size}, expected {self.n}")
+        D = self.depth
+        sf = np.empty(D, dtype=np.int32)
+        sb = np.empty(D, dtype=np.int32)
+        ns = np.zeros(1, dtype=np.int32)
+        lv = np.empty(1 << D, dtype=np.float64)
+        lo = None
+        if leaf_of_bytes:
+            lo = np.empty(self.n, dtype={1: np.uint8, 2: np.uint16, 4: np.uint32}[leaf_of_bytes])
+        rc = self._L.cbgpu_grow_tree(self._s, _ptr(a), _ptr(t), self.n, _ptr(s),
+                                     0 if s is None else s.size, _ptr(sf), _ptr(sb), _ptr(ns), _ptr(lv),
+                                     _ptr(lo), leaf_of_bytes if lo is not None else 0)
+        _lib.check(rc)
+        k = int(ns[0])
+        return DeviceGrownTree(splits=[(int(sf[i]), int(sb[i]), False) for i in range(k)],
+                               leaf_values=lv,
+                               leaf_of=lo if lo is not None else np.zeros(0, dtype=np.uint32))
+
+    def end_device_training(self) -> None:
+        if self._s:
+            self._L.cbgpu_end(self._s)
+            self._s = C.c_void_p(None)
+
+    def __del__(self):
+        try:
+            self.end_device_training()
+        except Exception:
+            pass
+
+    # ---- session introspection ---------------------------------------------
+    def resident_approx(self) -> np.ndarray:
+        out = np.empty(self.n, dtype=np.float64)
+        _lib.check(self._L.cbgpu_session_approx(self._s, _ptr(out), self.n))
+        return out
+
+    def device_bins(self, n_features: int) -> np.ndarray:
+        out = np.empty((n_features, self.n), dtype=np.uint8)
+        _lib.check(self._L.cbgpu_session_bins(self._s, _ptr(out), self.n, n_features))
+        return out
+
+    def last_sample(self) -> np.ndarray:
+        out = np.empty(self.n, dtype=np.float64)
+        _lib.check(self._L.cbgpu_session_last_sample(self._s, _ptr(out), self.n))
+        return out
+
+    def set_profiling(self, on: bool) -> None:
+        _lib.check(self._L.cbgpu_session_set_profiling(self._s, 1 if on else 0))
+
+    def timing(self) -> np.ndarray:
+        """[tree ms, hist ms, derive+score ms, partition ms, der+bootstrap ms,
+        collectives ms, rows histogrammed, kernels launched] of the last tree."""
+        out = np.zeros(8, dtype=np.float64)
+        _lib.check(self._L.cbgpu_session_timing(self._s, _ptr(out)))
+        return out
+
+    def mark(self, slot: int) -> None:
+        """Record user event `slot` (0..3) on the session stream."""
+        _lib.check(self._L.cbgpu_session_mark(self._s, slot))
+
+    def elapsed_ms(self, a: int, b: int) -> float:
+        out = np.zeros(1, dtype=np.float64)
+        _lib.check(self._L.cbgpu_session_elapsed_ms(self._s, a, b, _ptr(out)))
+        return float(out[0])
+
+    def rng_state(self):
+        out = np.zeros(5, dtype=np.uint64)
+        _lib.check(self._L.cbgpu_session_rng_state(self._s, _ptr(out)))
+        return tuple(int(x) for x in out[:4]), int(out[4])
+
+
+# ---- building blocks -------------------------------------------------------
+
+def histogram(bins_row_major, g, h, leaf_of=None, n_leaves=1, n_bins=None) -> np.ndarray:
+    """Device level histogram, [leaf][feature][bin][2] (sum g, sum h)."""
+    L = _lib.load()
+    bins = np.ascontiguousarray(bins_row_major, dtype=np.uint8)
+    n, F = bins.shape
+    B = int(n_bins if n_bins is not None else (int(bins.max()) + 1 if bins.size else 1))
+    g = np.ascontiguousarray(g, dtype=np.float64)
+    h = np.ascontiguousarray(h, dtype=np.float64)
+    lo = None if leaf_of is None else np.ascontiguousarray(leaf_of, dtype=np.int32)
+    out = np.empty((n_leaves, F, B, 2), dtype=np.float64)
+    _lib.check(L.cbgpu_histogram(_ptr(bins), n, F, B, _ptr(g), _ptr(h), _ptr(lo), n_leaves, _ptr(out)))
+    return out
+
+
+def bootstrap_weights(kind: str, n: int, *, row_offset=0, rand_seed=0, rng_raw4=None, sample_rate=1.0,
+                      bagging_temperature=1.0, der_obj=None, mvs_lambda=0.0) -> np.ndarray:
+    """Device bootstrap weights (crates/cb-train/src/bootstrap.rs semantics)."""
+    L = _lib.load()
+    out = np.empty(n, dtype=np.float64)
+    raw = None if rng_raw4 is None else np.ascontiguousarray(rng_raw4, dtype=np.uint64)
+    d = None if der_obj is None else np.ascontiguousarray(der_obj, dtype=np.float64)
+    _lib.check(L.cbgpu_bootstrap_weights(BOOT[kind], n, row_offset, rand_seed & (2**64 - 1), _ptr(raw),
+                                         sample_rate, bagging_temperature, _ptr(d), mvs_lambda, _ptr(out)))
+    return out

@@ -1,0 +1,217 @@
+/*
+ * cbgpu.h -- C ABI of the B200-native oblivious-tree training path.
+ *
+ * This library replaces the device half of catboost_rs's compute seam: the
+ * `cb_compute::Runtime` trait methods that `cb_train`'s boosting loop calls
+ * (crates/cb-compute/src/runtime.rs:1410-1651).  A thin Rust shim implements
+ * `Runtime` on top of these entry points; everything
+ * above the seam (cb-train's loop, cb-data's pool, the fit/predict APIs)
+ * stays unchanged.
+ *
+ * Conventions (mirroring the seam, runtime.rs:899-906, 1410-1651):
+ *  - plain pointers and sizes; inputs are borrowed for the call only;
+ *  - every entry point returns a cbgpu_status; CBGPU_DECLINED means "decline
+ *    to the CPU grower" (the trait's Ok(false) / Ok(None));
+ *  - on any other non-zero status cbgpu_last_error() returns a message
+ *    (thread-local), the analogue of the trait's CbError;
+ *  - sessions are not thread-safe; the caller serializes calls per session
+ *    (the reference wraps its session in a Mutex, gpu_backend.rs:47-67).
+ */
+#ifndef CBGPU_H
+#define CBGPU_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define CBGPU_API __attribute__((visibility("default")))
+#else
+#define CBGPU_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    CBGPU_OK = 0,
+    CBGPU_DECLINED = 1,       /* outside the covered regime: use the CPU grower */
+    CBGPU_ERR_INVALID = 2,    /* LengthMismatch / Degenerate / OutOfRange */
+    CBGPU_ERR_CUDA = 3,       /* CUDA runtime error */
+    CBGPU_ERR_OOM = 4,        /* device allocation failed */
+    CBGPU_ERR_NCCL = 5,       /* collective failed or timed out */
+    CBGPU_ERR_DEVICE = 6,     /* a kernel raised its device error word */
+    CBGPU_ERR_NO_DEVICE = 7   /* no CUDA device / library built without one */
+} cbgpu_status;
+
+/* Loss (runtime.rs:57-70): only the device-covered subset. */
+typedef enum { CBGPU_LOSS_RMSE = 0, CBGPU_LOSS_LOGLOSS = 1, CBGPU_LOSS_CROSSENTROPY = 2 } cbgpu_loss;
+
+/* EScoreFunction (runtime.rs:834-864); Cosine is the default. */
+typedef enum {
+    CBGPU_SCORE_COSINE = 0, CBGPU_SCORE_L2 = 1, CBGPU_SCORE_SOLAR_L2 = 2, CBGPU_SCORE_NEWTON_L2 = 3,
+    CBGPU_SCORE_NEWTON_COSINE = 4, CBGPU_SCORE_LOO_L2 = 5, CBGPU_SCORE_SAT_L2 = 6
+} cbgpu_score_fn;
+
+/* DeviceBootstrapType (runtime.rs:1085-1097). */
+typedef enum {
+    CBGPU_BOOT_NO = 0, CBGPU_BOOT_BAYESIAN = 1, CBGPU_BOOT_BERNOULLI = 2, CBGPU_BOOT_MVS = 3,
+    CBGPU_BOOT_POISSON = 4
+} cbgpu_bootstrap;
+
+/* DeviceGrowPolicy (runtime.rs DeviceTrainConfig::grow_policy). */
+typedef enum { CBGPU_GROW_SYMMETRIC = 0, CBGPU_GROW_DEPTHWISE = 1, CBGPU_GROW_LOSSGUIDE = 2,
+               CBGPU_GROW_REGION = 3 } cbgpu_grow_policy;
+
+/* The scalar arguments of Runtime::begin_device_training{,_raw}
+ * (runtime.rs:1497, :1546) plus DeviceTrainConfig (runtime.rs:1259-1372)
+ * and the document-sharding placement of this rank. */
+typedef struct {
+    int32_t loss;                    /* cbgpu_loss */
+    int32_t depth;                   /* 1..16 (tree.rs MAX_DEPTH) */
+    int32_t boosting_type_is_plain;  /* must be 1 */
+    int32_t fold_count;              /* must be 1 */
+    int32_t score_function;          /* cbgpu_score_fn: Cosine or L2 are covered */
+    int64_t n;                       /* rows held by THIS rank */
+    int32_t n_features;
+    int32_t n_bins;                  /* max(border count) + 1; <= 256 */
+    double learning_rate;
+    double scaled_l2;                /* l2_leaf_reg * sum(weights) / n_total (leaf.rs:177) */
+    const double* weight;            /* [n] per-object weights, or NULL for unit weights */
+    /* DeviceTrainConfig */
+    int32_t grow_policy;             /* cbgpu_grow_policy: only SymmetricTree is covered */
+    int32_t bootstrap_type;          /* cbgpu_bootstrap */
+    float sample_rate;               /* Bernoulli / MVS subsample */
+    float bagging_temperature;       /* Bayesian temperature */
+    int32_t has_mvs_lambda;          /* 1: use mvs_lambda for every tree */
+    double mvs_lambda;
+    uint64_t rng_seed;               /* the fit's random_seed (main TFastRng64 stream) */
+    double bias;                     /* starting approximant for the resident approx */
+    int32_t sample_from_host;        /* 1: grow_tree receives the bootstrap multiplier */
+    double random_strength;          /* must be 0 (the device gate, boosting.rs:5789-6010) */
+    /* placement (1 GPU: rank 0 of 1, row_offset 0, n_total == n) */
+    int32_t device;                  /* CUDA ordinal for this rank */
+    int32_t rank;
+    int32_t world_size;
+    int64_t row_offset;              /* global index of this rank's first row */
+    int64_t n_total;                 /* rows over all ranks */
+    const uint8_t* nccl_unique_id;   /* 128 bytes from cbgpu_nccl_unique_id when world_size > 1 */
+    /* [n_features] border count per feature for cbgpu_begin (split candidates
+     * are borders 0..count-1), or NULL: n_bins - 1 candidates for every
+     * feature, as the reference device scorer does (kernels.rs:4687-4712).
+     * cbgpu_begin_raw takes the counts from its border lists. */
+    const int32_t* border_counts;
+} cbgpu_begin_args;
+
+typedef struct cbgpu_session cbgpu_session;
+
+/* Runtime::begin_device_training (runtime.rs:1497): host-quantized bins,
+ * FEATURE-major u32 `bins_feature_major[f * n + i]`.  `*out` is NULL when
+ * the call declines. */
+CBGPU_API int cbgpu_begin(const cbgpu_begin_args* args, const uint32_t* bins_feature_major,
+                cbgpu_session** out);
+
+/* Runtime::begin_device_training_raw (runtime.rs:1546): raw f32 columns
+ * (`float_columns[f]` points at n values) and per-feature ascending f64
+ * borders, quantized on the device with the reference's bin_of rule
+ * (histogram.rs:159-165; NaN -> bin 0, or the top bin under the f32::MAX
+ * nan_mode=Max sentinel). */
+CBGPU_API int cbgpu_begin_raw(const cbgpu_begin_args* args, const float* const* float_columns,
+                    const double* borders_flat, const int32_t* border_counts,
+                    cbgpu_session** out);
+
+/* Runtime::grow_tree_on_device (runtime.rs:1629) for the SymmetricTree arm.
+ *  approx  [n] the caller's raw approximant, or NULL to use the session's
+ *          resident approximant (initialised to args.bias, advanced by
+ *          learning_rate * leaf value after every tree, as the reference
+ *          session does, session.rs:2560-2760);
+ *  target  [n] uploaded on the first call only;
+ *  sample  [sample_len] per-object bootstrap multiplier (control ? w : 0);
+ *          sample_len must be n when the session was opened with
+ *          sample_from_host, else 0 (session.rs:2405-2428);
+ * Outputs (DeviceGrownTree, runtime.rs:989-1059):
+ *  split_feature / split_bin  [depth] feature and border index per level
+ *          (level l is leaf bit l); the split passes iff bin > split_bin;
+ *  n_splits                   splits written;
+ *  leaf_values [2^depth]      raw leaf deltas, NOT scaled by learning_rate;
+ *  leaf_of / leaf_of_bytes    optional per-object leaf ids (1 = u8, 2 = u16,
+ *                             4 = u32; 0 / NULL = not requested). */
+CBGPU_API int cbgpu_grow_tree(cbgpu_session* s, const double* approx, const double* target, int64_t n,
+                    const double* sample, int64_t sample_len, int32_t* split_feature,
+                    int32_t* split_bin, int32_t* n_splits, double* leaf_values, void* leaf_of,
+                    int32_t leaf_of_bytes);
+
+/* Runtime::end_device_training (runtime.rs:1648): frees the session. */
+CBGPU_API int cbgpu_end(cbgpu_session* s);
+
+/* Runtime::compute_gradients (runtime.rs:1431) for RMSE / Logloss /
+ * CrossEntropy at approx_dimension 1 (loss.rs:35-80), on the device. */
+CBGPU_API int cbgpu_compute_gradients(int32_t loss, const double* approx, const double* target, int64_t n,
+                            double* der1, double* der2);
+
+/* Thread-local message for the last non-OK status (CbError analogue). */
+CBGPU_API const char* cbgpu_last_error(void);
+
+/* ---- session introspection (tests / drivers) ------------------------- */
+
+/* Copy the session's resident approximant to the host (flushes the pending
+ * learning_rate * leaf update first). */
+CBGPU_API int cbgpu_session_approx(cbgpu_session* s, double* out, int64_t n);
+
+/* Copy the device-quantized bins back, feature-major u8 [F][n]. */
+CBGPU_API int cbgpu_session_bins(cbgpu_session* s, uint8_t* out_feature_major, int64_t n, int32_t n_features);
+
+/* Copy the per-object score-channel bootstrap weights of the last tree
+ * (control ? sample_weight : 0) to the host. */
+CBGPU_API int cbgpu_session_last_sample(cbgpu_session* s, double* out, int64_t n);
+
+/* Last tree: [0] device ms of the whole tree (always measured); with
+ * profiling on, device ms of [1] histogram kernels, [2] derive + score,
+ * [3] partition / route, [4] derivative + bootstrap, [5] collectives; always
+ * [6] rows histogrammed over all levels and [7] kernels launched. */
+CBGPU_API int cbgpu_session_timing(cbgpu_session* s, double* out8);
+
+/* Record user event `slot` (0..3) on the session's stream, and read the
+ * device milliseconds between two recorded slots (synchronizes on `b`). */
+CBGPU_API int cbgpu_session_mark(cbgpu_session* s, int32_t slot);
+CBGPU_API int cbgpu_session_elapsed_ms(cbgpu_session* s, int32_t a, int32_t b, double* out);
+
+/* Enable (1) / disable (0) per-stage CUDA-event timing (off by default). */
+CBGPU_API int cbgpu_session_set_profiling(cbgpu_session* s, int32_t enabled);
+
+/* Host TFastRng64 replica of the session's main stream (raw state + calls),
+ * so a driver can check it stays in lockstep with cb-train's RNG. */
+CBGPU_API int cbgpu_session_rng_state(cbgpu_session* s, uint64_t* out5);
+
+/* ---- building blocks (each is a standalone device computation) ------- */
+
+/* One level histogram over `n` rows: bins row-major u8 [n][n_features],
+ * g/h [n] f64 score channels, leaf_of [n] (or NULL = all leaf 0).  Output
+ * hist[leaf][feature][bin][2] f64 (channel 0 = sum g, 1 = sum h), computed
+ * with exact int64 fixed-point accumulation (crates/cb-compute/src/
+ * histogram.rs:239-294 semantics). */
+CBGPU_API int cbgpu_histogram(const uint8_t* bins_row_major, int64_t n, int32_t n_features, int32_t n_bins,
+                    const double* g, const double* h, const int32_t* leaf_of, int32_t n_leaves,
+                    double* out_hist);
+
+/* Bootstrap weights exactly as crates/cb-train/src/bootstrap.rs produces them
+ * for global rows [row_offset, row_offset + n):
+ *  Bayesian: rand_seed = the main-stream draw; out = sample weight.
+ *  Bernoulli: rng_raw4 = main-stream raw state before the n_total draws;
+ *             out = 1.0 / 0.0 control mask.
+ *  MVS: der_obj [n] (|w * der1|), lambda, rand_seed; out = sample weight
+ *       (row_offset must be a multiple of 8192). */
+CBGPU_API int cbgpu_bootstrap_weights(int32_t type, int64_t n, int64_t row_offset, uint64_t rand_seed,
+                            const uint64_t* rng_raw4, float sample_rate, float bagging_temperature,
+                            const double* der_obj, double lambda, double* out);
+
+/* NCCL unique id (128 bytes) for world_size > 1 sessions. */
+CBGPU_API int cbgpu_nccl_unique_id(uint8_t* out128);
+
+/* Library version string. */
+CBGPU_API const char* cbgpu_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* CBGPU_H */
