@@ -377,7 +377,7 @@ void launch_mvs(int64_t n, int64_t row_offset, const double* wd1, double lambda,
 }
 
 // ============================================================================
-// fused apply + derivatives + score channels (loss.rs:35-80, boosting.rs:7450-7732)
+// fused apply + derivatives (loss.rs:35-80, boosting.rs:7450-7732)
 // ============================================================================
 
 __device__ __forceinline__ void block_max4(double m[4], TreeState* ts) {
@@ -402,12 +402,18 @@ __device__ __forceinline__ void block_max4(double m[4], TreeState* ts) {
     }
 }
 
+__device__ __forceinline__ double sample_of(int s_mode, const float* sw32, const double* sw64, int64_t i) {
+    return s_mode == 0 ? 1.0 : (s_mode == 1 ? (double)sw32[i] : sw64[i]);
+}
+
+// approx += lr * leaf value of the previous tree (when pending), then
+// der1 (RMSE t - a; Logloss t - (1 - 1/(1 + e^a))), wd1 = der1 * w, and the
+// maxima of |g| = |wd1 * s|, |h| = |w * s|, |wd1|, |w| for the fixed-point scales.
 __global__ void __launch_bounds__(256) der_kernel(
     int64_t n, int loss, double* __restrict__ approx, const double* __restrict__ target,
     const double* __restrict__ weight, const uint16_t* __restrict__ leaf,
     const double* __restrict__ lrv, int s_mode, const float* __restrict__ sw32,
-    const double* __restrict__ sw64, double* __restrict__ wd1, double2* __restrict__ stats,
-    TreeState* ts, bool defer) {
+    const double* __restrict__ sw64, double* __restrict__ wd1, TreeState* ts, bool defer) {
     double m[4] = {0.0, 0.0, 0.0, 0.0};
     bool bad = false;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
@@ -433,9 +439,8 @@ __global__ void __launch_bounds__(256) der_kernel(
         m[3] = fmax(m[3], fabs(w));
         bad |= !isfinite(wd);
         if (!defer) {
-            const double s = s_mode == 0 ? 1.0 : (s_mode == 1 ? (double)sw32[i] : sw64[i]);
+            const double s = sample_of(s_mode, sw32, sw64, i);
             const double g = __dmul_rn(wd, s), h = __dmul_rn(w, s);
-            stats[i] = make_double2(g, h);
             m[0] = fmax(m[0], fabs(g));
             m[1] = fmax(m[1], fabs(h));
             bad |= !isfinite(g) || !isfinite(h);
@@ -447,42 +452,41 @@ __global__ void __launch_bounds__(256) der_kernel(
 
 void launch_der(int64_t n, int loss, double* approx, const double* target, const double* weight,
                 const uint16_t* leaf, const double* lrv, int s_mode, const float* sw32,
-                const double* sw64, double* wd1, double2* stats, TreeState* ts, bool defer,
-                cudaStream_t st) {
+                const double* sw64, double* wd1, TreeState* ts, bool defer, cudaStream_t st) {
     int64_t blocks = (n + 255) / 256;
     if (blocks > 148 * 8) blocks = 148 * 8;
     if (blocks < 1) blocks = 1;
     der_kernel<<<(unsigned)blocks, 256, 0, st>>>(n, loss, approx, target, weight, leaf, lrv, s_mode,
-                                                 sw32, sw64, wd1, stats, ts, defer);
+                                                 sw32, sw64, wd1, ts, defer);
 }
 
-__global__ void __launch_bounds__(256) stats_kernel(int64_t n, const double* __restrict__ wd1,
-                                                    const double* __restrict__ weight,
-                                                    const float* __restrict__ sw32,
-                                                    double2* __restrict__ stats, TreeState* ts) {
+// Maxima of |g| and |h| once an MVS sample exists.
+__global__ void __launch_bounds__(256) max_gh_kernel(int64_t n, const double* __restrict__ wd1,
+                                                     const double* __restrict__ weight,
+                                                     const float* __restrict__ sw32, TreeState* ts) {
     double m[4] = {0.0, 0.0, 0.0, 0.0};
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
          i += (int64_t)gridDim.x * blockDim.x) {
         const double w = weight ? weight[i] : 1.0;
         const double s = (double)sw32[i];
-        const double g = __dmul_rn(wd1[i], s), h = __dmul_rn(w, s);
-        stats[i] = make_double2(g, h);
-        m[0] = fmax(m[0], fabs(g));
-        m[1] = fmax(m[1], fabs(h));
+        m[0] = fmax(m[0], fabs(__dmul_rn(wd1[i], s)));
+        m[1] = fmax(m[1], fabs(__dmul_rn(w, s)));
     }
     block_max4(m, ts);
 }
 
-void launch_stats_from_sample(int64_t n, const double* wd1, const double* weight, const float* sw32,
-                              double2* stats, TreeState* ts, cudaStream_t st) {
+void launch_max_gh(int64_t n, const double* wd1, const double* weight, const float* sw32, TreeState* ts,
+                   cudaStream_t st) {
     int64_t blocks = (n + 255) / 256;
     if (blocks > 148 * 8) blocks = 148 * 8;
     if (blocks < 1) blocks = 1;
-    stats_kernel<<<(unsigned)blocks, 256, 0, st>>>(n, wd1, weight, sw32, stats, ts);
+    max_gh_kernel<<<(unsigned)blocks, 256, 0, st>>>(n, wd1, weight, sw32, ts);
 }
 
-// Fixed-point scale per channel: 2^s with max|v| * n_total * 2^s < 2^62, so any
-// partial sum of rounded values stays below 2^63.
+// Fixed-point scales.  Score channels (g, h): 2^s with max|v| * 2^s < 2^33, so a
+// row value splits into hi = v >> 17 (|hi| <= 2^16) and lo = v & (2^17 - 1) whose
+// 32-bit sums over a kChunkRows-row work item cannot overflow; resolution is
+// 2^-33 of the largest value.  Leaf channels: max|v| * n_total * 2^s < 2^62.
 __global__ void scales_kernel(TreeState* ts, int64_t n_total) {
     if (threadIdx.x != 0) return;
     for (int c = 0; c < 4; ++c) {
@@ -490,8 +494,13 @@ __global__ void scales_kernel(TreeState* ts, int64_t n_total) {
         int s = 0;
         if (m > 0.0) {
             int e;
-            frexp(m * (double)(n_total > 0 ? n_total : 1), &e);
-            s = 62 - e;
+            if (c < 2) {
+                frexp(m, &e);
+                s = kPackBits - e;
+            } else {
+                frexp(m * (double)(n_total > 0 ? n_total : 1), &e);
+                s = 62 - e;
+            }
             if (s > 1000) s = 1000;
             if (s < -1000) s = -1000;
         }
@@ -502,6 +511,41 @@ __global__ void scales_kernel(TreeState* ts, int64_t n_total) {
 
 void launch_scales(TreeState* ts, int64_t n_total, cudaStream_t st) {
     scales_kernel<<<1, 32, 0, st>>>(ts, n_total);
+}
+
+// Per row: g = wd1 * s, h = w * s (the CPU's score channels, boosting.rs:7700-7732),
+// rounded once to fixed point and split into the (lo, hi) parts the histogram
+// accumulates: {g_lo, g_hi, h_lo, h_hi}.
+__device__ __forceinline__ void split_fixed(double v, double scale, uint32_t& lo, uint32_t& hi) {
+    const long long q = __double2ll_rn(__dmul_rn(v, scale));
+    lo = (uint32_t)(q & ((1ll << kPackSplit) - 1));
+    hi = (uint32_t)(int32_t)(q >> kPackSplit);
+}
+
+__global__ void __launch_bounds__(256) pack_stats_kernel(int64_t n, const double* __restrict__ wd1,
+                                                         const double* __restrict__ weight, int s_mode,
+                                                         const float* __restrict__ sw32,
+                                                         const double* __restrict__ sw64,
+                                                         const TreeState* __restrict__ ts,
+                                                         uint4* __restrict__ qstats) {
+    const double sg = ts->sc.scale[0], sh = ts->sc.scale[1];
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const double w = weight ? weight[i] : 1.0;
+        const double s = sample_of(s_mode, sw32, sw64, i);
+        uint4 o;
+        split_fixed(__dmul_rn(wd1[i], s), sg, o.x, o.y);
+        split_fixed(__dmul_rn(w, s), sh, o.z, o.w);
+        qstats[i] = o;
+    }
+}
+
+void launch_pack_stats(int64_t n, const double* wd1, const double* weight, int s_mode, const float* sw32,
+                       const double* sw64, const TreeState* ts, uint4* qstats, cudaStream_t st) {
+    int64_t blocks = (n + 255) / 256;
+    if (blocks > 148 * 8) blocks = 148 * 8;
+    if (blocks < 1) return;
+    pack_stats_kernel<<<(unsigned)blocks, 256, 0, st>>>(n, wd1, weight, s_mode, sw32, sw64, ts, qstats);
 }
 
 __global__ void apply_kernel(int64_t n, double* __restrict__ approx, const uint16_t* __restrict__ leaf,
@@ -523,91 +567,151 @@ void launch_apply(int64_t n, double* approx, const uint16_t* leaf, const double*
 // histogram (the hot kernel)
 // ============================================================================
 //
-// Grid (chunk, feature tile).  A block owns one work item (rows of ONE leaf)
-// and one 32-feature tile; lane f of every warp owns feature tile*32+f, so the
-// 32 lanes of a shared-memory update always hit 32 different feature
-// histograms and never the same address.  Each warp reads a row's 32-byte tile
-// slice (one sector) and broadcasts the row's (g, h).  Channel values are
-// converted to int64 fixed point and accumulated with shared-memory atomics,
-// then merged into the global built histogram with int64 atomics: the sum is
-// exact and independent of ordering.
+// Grid (work item, feature tile).  A block owns one work item (<= kChunkRows
+// rows of ONE leaf) and one 32-feature tile; lane f of every warp owns feature
+// tile*32+f.  Shared memory holds the tile histogram as u32 words laid out
+// [bin][part][lane] (part = g_lo, g_hi, h_lo, h_hi), so lane f always touches
+// bank f: the 32 updates of a warp are bank-conflict free whatever the bins.
+// Each update is four 32-bit shared reductions of the row's pre-split fixed
+// point parts; the parts of a work item cannot overflow 32 bits, and the flush
+// recombines them into exact int64 sums merged with global atomics.  Integer
+// sums make the result independent of ordering, launch geometry and GPU count.
 
 void launch_zero(void* p, size_t bytes, cudaStream_t st) {
     if (bytes) cudaMemsetAsync(p, 0, bytes, st);
 }
 
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+    const unsigned d = (unsigned)__cvta_generic_to_shared(smem_dst);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(d), "l"(gmem_src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
+
+// Each warp streams its rows in groups of 32 through a kHistStages-deep ring
+// of shared-memory stages: lane l copies row l's 32-byte tile slice (2 x 16 B)
+// and its 16-byte packed stats with cp.async, so one warp instruction moves
+// 512 B and many groups are in flight.  A staged group is then consumed with
+// lane = feature: one byte load of (row, lane), one broadcast load of the row's
+// stats and four conflict-free 32-bit shared reductions.
 template <bool kGather>
-__global__ void __launch_bounds__(kHistThreads) hist_kernel(
+__global__ void __launch_bounds__(kHistThreads, 2) hist_kernel(
     const uint8_t* __restrict__ bins_rm, int32_t F_pad, int32_t F, int32_t B,
-    const double2* __restrict__ stats, const uint32_t* __restrict__ perm,
+    const uint4* __restrict__ qstats, const uint32_t* __restrict__ perm,
     const HistChunk* __restrict__ chunks, const uint32_t* __restrict__ n_chunks,
-    const TreeState* __restrict__ ts, ull* __restrict__ built) {
-    extern __shared__ ull hsm[];  // [kTile][B][2]
+    ull* __restrict__ built) {
+    extern __shared__ __align__(16) uint32_t hs[];  // [B][4][32] then the staging ring
     if (blockIdx.x >= *n_chunks) return;
     const HistChunk ck = chunks[blockIdx.x];
     const int tile = blockIdx.y;
-    const int cells = kTile * B * 2;
-    for (int k = threadIdx.x; k < cells; k += blockDim.x) hsm[k] = 0ull;
-    __syncthreads();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int nwarps = blockDim.x >> 5;
+    constexpr int kWarps = kHistThreads / 32;
+    uint8_t* sbins = (uint8_t*)(hs + B * 128) + (size_t)warp * kHistStages * 32 * 32;
+    uint4* sstat = (uint4*)((uint8_t*)(hs + B * 128) + (size_t)kWarps * kHistStages * 32 * 32) +
+                   (size_t)warp * kHistStages * 32;
+    for (int k = threadIdx.x; k < B * 128; k += blockDim.x) hs[k] = 0u;
+    __syncthreads();
+
     const int f = tile * kTile + lane;
     const bool active = f < F;
-    const double sg = ts->sc.scale[0], sh = ts->sc.scale[1];
-    const uint8_t* colp = bins_rm + f;
-    ull* my = hsm + lane * B * 2;
+    uint32_t* my = hs + lane;
     const uint32_t start = ck.start, len = ck.len;
-    uint32_t r = warp;
-    // 4 rows in flight per warp for memory-level parallelism
-    for (; r + 3 * nwarps < len; r += 4 * nwarps) {
-        uint32_t i[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            uint32_t j = start + r + u * nwarps;
-            i[u] = kGather ? __ldg(perm + j) : j;
+    const uint32_t n_groups = (len + 31) >> 5;
+    const uint8_t* tile_base = bins_rm + tile * kTile;
+
+    // groups of this warp: g = warp, warp + kWarps, ...
+    auto row_of = [&](uint32_t g) -> uint32_t {  // row index for lane's row of group g (or ~0)
+        const uint32_t r = (g << 5) + lane;
+        if (g >= n_groups || r >= len) return 0xffffffffu;
+        return kGather ? __ldg(perm + start + r) : start + r;
+    };
+    auto issue = [&](uint32_t g, uint32_t i, int st) {
+        if (i != 0xffffffffu) {
+            uint8_t* d = sbins + ((size_t)st * 32 + lane) * 32;
+            const uint8_t* src = tile_base + (size_t)i * F_pad;
+            cp_async16(d, src);
+            cp_async16(d + 16, src + 16);
+            cp_async16(sstat + st * 32 + lane, qstats + i);
         }
-        double2 s[4];
-        uint32_t b[4];
+        cp_async_commit();
+    };
+    uint32_t g = warp;
+    // prologue: stages 0 .. kHistStages-2
+    uint32_t inext = row_of(g);
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            s[u] = __ldg(stats + i[u]);
-            b[u] = active ? __ldg(colp + (size_t)i[u] * F_pad) : 0u;
-        }
+    for (int p = 0; p < kHistStages - 1; ++p) {
+        issue(g + p * kWarps, inext, p);
+        inext = row_of(g + (p + 1) * kWarps);
+    }
+    int st = 0;
+    for (; g < n_groups; g += kWarps) {
+        // keep kHistStages - 1 groups in flight
+        const int st_issue = (st + kHistStages - 1) % kHistStages;
+        issue(g + (kHistStages - 1) * kWarps, inext, st_issue);
+        inext = row_of(g + kHistStages * kWarps);
+        cp_async_wait<kHistStages - 1>();
+        __syncwarp();
+        const uint32_t cnt = len - (g << 5) < 32u ? len - (g << 5) : 32u;
+        const uint8_t* sb = sbins + (size_t)st * 32 * 32 + lane;
+        const uint4* ss = sstat + st * 32;
         if (active) {
+            uint32_t u = 0;
+            for (; u + 4 <= cnt; u += 4) {
+                uint32_t b[4];
+                uint4 s[4];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                long long qg = __double2ll_rn(__dmul_rn(s[u].x, sg));
-                long long qh = __double2ll_rn(__dmul_rn(s[u].y, sh));
-                atomicAdd(my + 2 * b[u], (ull)qg);
-                atomicAdd(my + 2 * b[u] + 1, (ull)qh);
+                for (int v = 0; v < 4; ++v) {
+                    b[v] = sb[(u + v) * 32];
+                    s[v] = ss[u + v];
+                }
+#pragma unroll
+                for (int v = 0; v < 4; ++v) {
+                    uint32_t* c = my + b[v] * 128;
+                    atomicAdd(c, s[v].x);
+                    atomicAdd(c + 32, s[v].y);
+                    atomicAdd(c + 64, s[v].z);
+                    atomicAdd(c + 96, s[v].w);
+                }
+            }
+            for (; u < cnt; ++u) {
+                const uint32_t bb = sb[u * 32];
+                const uint4 s = ss[u];
+                uint32_t* c = my + bb * 128;
+                atomicAdd(c, s.x);
+                atomicAdd(c + 32, s.y);
+                atomicAdd(c + 64, s.z);
+                atomicAdd(c + 96, s.w);
             }
         }
+        __syncwarp();  // the stage is refilled next iteration
+        st = (st + 1) % kHistStages;
     }
-    for (; r < len; r += nwarps) {
-        uint32_t j = start + r;
-        uint32_t i = kGather ? __ldg(perm + j) : j;
-        double2 s = __ldg(stats + i);
-        if (active) {
-            uint32_t b = __ldg(colp + (size_t)i * F_pad);
-            atomicAdd(my + 2 * b, (ull)__double2ll_rn(__dmul_rn(s.x, sg)));
-            atomicAdd(my + 2 * b + 1, (ull)__double2ll_rn(__dmul_rn(s.y, sh)));
-        }
-    }
+    cp_async_wait<0>();
     __syncthreads();
     const int nf = F - tile * kTile < kTile ? F - tile * kTile : kTile;
     ull* out = built + ((size_t)ck.slot * F + (size_t)tile * kTile) * B * 2;
-    for (int k = threadIdx.x; k < nf * B * 2; k += blockDim.x) {
-        ull v = hsm[k];
-        if (v) atomicAdd(out + k, v);
+    for (int k = threadIdx.x; k < B * 32; k += blockDim.x) {
+        const int b = k >> 5, l = k & 31;
+        if (l >= nf) continue;
+        const uint32_t* c = hs + b * 128 + l;
+        const long long gsum = (long long)(int32_t)c[32] * (1ll << kPackSplit) + (long long)c[0];
+        const long long hsum = (long long)(int32_t)c[96] * (1ll << kPackSplit) + (long long)c[64];
+        ull* o = out + ((size_t)l * B + b) * 2;
+        if (gsum) atomicAdd(o, (ull)gsum);
+        if (hsum) atomicAdd(o + 1, (ull)hsum);
     }
 }
 
-void launch_hist(const uint8_t* bins_rm, int32_t F_pad, int32_t F, int32_t B,
-                 const double2* stats, const uint32_t* perm, const HistChunk* chunks,
-                 const uint32_t* n_chunks, uint32_t max_chunks, const TreeState* ts, ull* built,
-                 cudaStream_t st) {
+size_t hist_smem_bytes(int32_t B) {
+    return sizeof(uint32_t) * (size_t)B * 128 + (size_t)(kHistThreads / 32) * kHistStages * 32 * (32 + 16);
+}
+
+void launch_hist(const uint8_t* bins_rm, int32_t F_pad, int32_t F, int32_t B, const uint4* qstats,
+                 const uint32_t* perm, const HistChunk* chunks, const uint32_t* n_chunks,
+                 uint32_t max_chunks, ull* built, cudaStream_t st) {
     if (max_chunks == 0) return;
-    size_t smem = sizeof(ull) * kTile * B * 2;
+    const size_t smem = hist_smem_bytes(B);
     static bool attr = false;
     if (!attr) {
         cudaFuncSetAttribute(hist_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
@@ -616,18 +720,20 @@ void launch_hist(const uint8_t* bins_rm, int32_t F_pad, int32_t F, int32_t B,
     }
     dim3 grid(max_chunks, (unsigned)((F + kTile - 1) / kTile));
     if (perm)
-        hist_kernel<true><<<grid, kHistThreads, smem, st>>>(bins_rm, F_pad, F, B, stats, perm, chunks,
-                                                             n_chunks, ts, built);
+        hist_kernel<true><<<grid, kHistThreads, smem, st>>>(bins_rm, F_pad, F, B, qstats, perm, chunks,
+                                                             n_chunks, built);
     else
-        hist_kernel<false><<<grid, kHistThreads, smem, st>>>(bins_rm, F_pad, F, B, stats, perm,
-                                                              chunks, n_chunks, ts, built);
+        hist_kernel<false><<<grid, kHistThreads, smem, st>>>(bins_rm, F_pad, F, B, qstats, perm, chunks,
+                                                              n_chunks, built);
 }
 
 // Work list for the level: level 0 = all rows (identity order) in one slot;
 // level l >= 1 = for each parent p the smaller child's leaf-sorted segment
-// into slot p, cut into kChunkRows pieces.
+// into slot p, cut into kChunkRows pieces.  Level 0 also initialises the
+// segment tables to the single all-rows segment.
 __global__ void make_chunks_kernel(int level, uint32_t* __restrict__ seg_off,
-                                   uint32_t* __restrict__ seg_cnt,
+                                   uint32_t* __restrict__ seg_cnt, uint32_t* __restrict__ mem_start,
+                                   uint32_t* __restrict__ mem_leaf,
                                    const uint8_t* __restrict__ small_side, int64_t n0,
                                    HistChunk* __restrict__ chunks, uint32_t* __restrict__ n_chunks,
                                    TreeState* ts) {
@@ -641,8 +747,10 @@ __global__ void make_chunks_kernel(int level, uint32_t* __restrict__ seg_off,
         }
         if (threadIdx.x == 0) {
             *n_chunks = nch;
-            seg_off[0] = 0u;  // level 0: one segment holding every row
+            seg_off[0] = 0u;
             seg_cnt[0] = (uint32_t)n0;
+            mem_start[0] = 0u;
+            mem_leaf[0] = 0u;
             ts->hist_rows[0] = (uint32_t)n0;
         }
         return;
@@ -662,9 +770,8 @@ __global__ void make_chunks_kernel(int level, uint32_t* __restrict__ seg_off,
     for (uint32_t p = p0; p < p0 + per && p < half; ++p) {
         uint32_t c = small_side[p] ? p + half : p;
         uint32_t off = seg_off[c], ln = seg_cnt[c];
-        for (uint32_t st = 0; st < ln; st += kChunkRows) {
+        for (uint32_t st = 0; st < ln; st += kChunkRows)
             chunks[base++] = HistChunk{p, off + st, ln - st < (uint32_t)kChunkRows ? ln - st : (uint32_t)kChunkRows, 0u};
-        }
     }
     if (threadIdx.x == 0) {
         *n_chunks = tot;
@@ -672,11 +779,11 @@ __global__ void make_chunks_kernel(int level, uint32_t* __restrict__ seg_off,
     }
 }
 
-void launch_make_chunks(int level, uint32_t* seg_off, uint32_t* seg_cnt,
-                        const uint8_t* small_side, int64_t n_level0, HistChunk* chunks,
-                        uint32_t* n_chunks, TreeState* ts, cudaStream_t st) {
-    make_chunks_kernel<<<1, 1024, 0, st>>>(level, seg_off, seg_cnt, small_side, n_level0, chunks,
-                                           n_chunks, ts);
+void launch_make_chunks(int level, uint32_t* seg_off, uint32_t* seg_cnt, uint32_t* mem_start,
+                        uint32_t* mem_leaf, const uint8_t* small_side, int64_t n_level0,
+                        HistChunk* chunks, uint32_t* n_chunks, TreeState* ts, cudaStream_t st) {
+    make_chunks_kernel<<<1, 1024, 0, st>>>(level, seg_off, seg_cnt, mem_start, mem_leaf, small_side,
+                                           n_level0, chunks, n_chunks, ts);
 }
 
 // ============================================================================
@@ -746,7 +853,7 @@ void launch_derive_prefix(int level, int32_t F, int32_t B, const ull* built, con
 // folded in the CPU's canonical order (false children 0..Q-1, then true).
 // The last block to finish reduces the per-feature winners (no spin wait).
 // ============================================================================
-__global__ void __launch_bounds__(256) score_kernel(int level, int32_t F, int32_t B,
+__global__ void __launch_bounds__(128) score_kernel(int level, int32_t F, int32_t B,
                                                     const ull* __restrict__ cur,
                                                     const int32_t* __restrict__ border_counts,
                                                     double l2, int score_fn,
@@ -785,7 +892,6 @@ __global__ void __launch_bounds__(256) score_kernel(int level, int32_t F, int32_
             bbin = b;
         }
     }
-    // block argmax
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
@@ -807,7 +913,6 @@ __global__ void __launch_bounds__(256) score_kernel(int level, int32_t F, int32_
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    // final reduction over features, lowest feature on ties
     double fb = -INFINITY;
     int fi = 0x7fffffff;
     for (int ff = threadIdx.x; ff < F; ff += blockDim.x) {
@@ -850,13 +955,16 @@ void launch_score(int level, int32_t F, int32_t B, const ull* cur, const int32_t
 }
 
 // ============================================================================
-// partition: stable per-segment split of the leaf-sorted row order so the
-// next level can gather each child's rows contiguously.
-//  P1 (count): per tile of kPartTile positions: true-flag count, and for each
-//     segment that starts / ends inside the tile the in-tile prefix there.
-//  P2 (scan):  tile offsets, per-segment true counts, child counts, next
-//     segment table.
-//  P3 (scatter): destination of every position, new leaf ids.
+// partition: stable per-segment split of the leaf-sorted row order so the next
+// level can read each child's rows contiguously.  Segments (one per leaf) are
+// contiguous position ranges; mem_start/mem_leaf list them in position order,
+// so a position's leaf is found by offset, without per-row leaf reads.
+//  P1 (count):   per tile of kPartTile positions the true-flag count, and the
+//                in-tile prefix at every segment start / end inside the tile.
+//  P2 (scan):    tile offsets, per-segment true counts, child counts and the
+//                next level's segment tables.
+//  P3 (scatter): destination of every position.
+// The last level instead writes the final leaf id of every row (natural order).
 // ============================================================================
 
 struct PartView {
@@ -874,16 +982,45 @@ __device__ __forceinline__ PartView part_view(const TreeState* ts, int level, co
     return v;
 }
 
+// Index of the segment (in position order) holding position j: the last k with
+// mem_start[k] <= j (empty segments share their successor's start).
+__device__ __forceinline__ int seg_of(const uint32_t* __restrict__ mem_start, int K, uint32_t j) {
+    int lo = 0, hi = K - 1;
+    while (lo < hi) {
+        int mid = (lo + hi + 1) >> 1;
+        if (mem_start[mid] <= j) lo = mid; else hi = mid - 1;
+    }
+    return lo;
+}
+
+// Walks positions [j0, j0 + cnt) of this thread, calling fn(u, j, k) with the
+// segment index k of each position.
+template <typename Fn>
+__device__ __forceinline__ void walk_segments(const uint32_t* __restrict__ mem_start, int K, uint32_t j0,
+                                              int cnt, Fn fn) {
+    int k = seg_of(mem_start, K, j0);
+    uint32_t next = k + 1 < K ? mem_start[k + 1] : 0xffffffffu;
+    for (int u = 0; u < cnt; ++u) {
+        const uint32_t j = j0 + u;
+        while (j >= next) {
+            ++k;
+            next = k + 1 < K ? mem_start[k + 1] : 0xffffffffu;
+        }
+        fn(u, j, k);
+    }
+}
+
 __global__ void __launch_bounds__(kPartThreads) part_count_kernel(
     int level, int64_t n, const uint8_t* __restrict__ bins_fm, int64_t n_stride,
-    const uint32_t* __restrict__ perm, const uint16_t* __restrict__ leaf,
+    const uint32_t* __restrict__ perm, const uint32_t* __restrict__ seg_cnt,
+    const uint32_t* __restrict__ mem_start, const uint32_t* __restrict__ mem_leaf,
     uint32_t* __restrict__ seg_start_blk, uint32_t* __restrict__ seg_start_part,
     uint32_t* __restrict__ seg_end_blk, uint32_t* __restrict__ seg_end_part,
     uint32_t* __restrict__ blk_true, const TreeState* __restrict__ ts) {
     __shared__ uint32_t s_idx[kPartTile];
     __shared__ uint32_t s_scan[40];
     const PartView pv = part_view(ts, level, bins_fm, n_stride);
-    const uint32_t mask = (1u << level) - 1u;
+    const int K = 1 << level;
     const int64_t base = (int64_t)blockIdx.x * kPartTile;
     for (int k = threadIdx.x; k < kPartTile; k += blockDim.x) {
         int64_t j = base + k;
@@ -891,72 +1028,46 @@ __global__ void __launch_bounds__(kPartThreads) part_count_kernel(
     }
     __syncthreads();
     const int k0 = threadIdx.x * kPartItems;
-    uint32_t flags = 0, qs[kPartItems];
+    const int64_t j0 = base + k0;
+    const int cnt_items = j0 >= n ? 0 : (int)(n - j0 < kPartItems ? n - j0 : kPartItems);
+    uint32_t flags = 0;
     int cnt = 0;
-#pragma unroll
-    for (int u = 0; u < kPartItems; ++u) {
-        uint32_t i = s_idx[k0 + u];
-        if (i != 0xffffffffu) {
-            uint32_t fl = (int32_t)pv.col[i] > pv.bin;
-            flags |= fl << u;
-            cnt += fl;
-            qs[u] = level ? (leaf[i] & mask) : 0u;
-        } else {
-            qs[u] = 0xffffffffu;
-        }
-    }
-    // leaf of the previous position (for segment-start detection)
-    uint32_t q_prev;
-    {
-        int64_t jp = base + k0 - 1;
-        if (jp < 0 || jp >= n) q_prev = 0xfffffffeu;  // no previous row, or no rows in this thread
-        else {
-            uint32_t ip = (k0 > 0) ? s_idx[k0 - 1] : (perm ? perm[jp] : (uint32_t)jp);
-            q_prev = level ? (leaf[ip] & mask) : 0u;
-        }
-    }
-    uint32_t q_next;
-    {
-        int64_t jn = base + k0 + kPartItems;
-        if (jn >= n) q_next = 0xfffffffdu;
-        else {
-            uint32_t in = (k0 + kPartItems < kPartTile) ? s_idx[k0 + kPartItems] : (perm ? perm[jn] : (uint32_t)jn);
-            q_next = level ? (leaf[in] & mask) : 0u;
-        }
+    for (int u = 0; u < cnt_items; ++u) {
+        const uint32_t fl = (int32_t)pv.col[s_idx[k0 + u]] > pv.bin;
+        flags |= fl << u;
+        cnt += fl;
     }
     uint32_t tot;
-    uint32_t excl = block_excl_scan<uint32_t>((uint32_t)cnt, s_scan, &tot);
-    uint32_t run = excl;
-#pragma unroll
-    for (int u = 0; u < kPartItems; ++u) {
-        uint32_t q = qs[u];
-        if (q == 0xffffffffu) break;
-        uint32_t before = (u == 0) ? q_prev : qs[u - 1];
-        uint32_t fl = (flags >> u) & 1u;
-        if (q != before) {
-            seg_start_blk[q] = blockIdx.x;
-            seg_start_part[q] = run;
-        }
-        run += fl;
-        uint32_t after = (u + 1 < kPartItems && qs[u + 1] != 0xffffffffu) ? qs[u + 1]
-                         : (u + 1 < kPartItems ? 0xfffffffcu : q_next);
-        if (q != after) {
-            seg_end_blk[q] = blockIdx.x;
-            seg_end_part[q] = run;  // inclusive
-        }
+    const uint32_t excl = block_excl_scan<uint32_t>((uint32_t)cnt, s_scan, &tot);
+    if (cnt_items > 0) {
+        uint32_t run = excl;
+        walk_segments(mem_start, K, (uint32_t)j0, cnt_items, [&](int u, uint32_t j, int k) {
+            const uint32_t q = mem_leaf[k];
+            const uint32_t s0 = mem_start[k];
+            const uint32_t fl = (flags >> u) & 1u;
+            if (j == s0) {
+                seg_start_blk[q] = blockIdx.x;
+                seg_start_part[q] = run;
+            }
+            run += fl;
+            if (j == s0 + seg_cnt[q] - 1) {
+                seg_end_blk[q] = blockIdx.x;
+                seg_end_part[q] = run;
+            }
+        });
     }
     if (threadIdx.x == 0) blk_true[blockIdx.x] = tot;
 }
 
-// Single block: tile offsets (in place), per-segment T_start and false count,
-// child counts and the next level's segment table.
 __global__ void __launch_bounds__(1024) part_scan_kernel(
     int level, uint32_t n_tiles, uint32_t* __restrict__ blk_true,
     const uint32_t* __restrict__ seg_off, const uint32_t* __restrict__ seg_cnt,
+    const uint32_t* __restrict__ mem_leaf,
     const uint32_t* __restrict__ seg_start_blk, const uint32_t* __restrict__ seg_start_part,
     const uint32_t* __restrict__ seg_end_blk, const uint32_t* __restrict__ seg_end_part,
     uint32_t* __restrict__ t_start, uint32_t* __restrict__ f_cnt, uint32_t* __restrict__ child_cnt,
-    uint32_t* __restrict__ seg_off_next, uint32_t* __restrict__ seg_cnt_next) {
+    uint32_t* __restrict__ seg_off_next, uint32_t* __restrict__ seg_cnt_next,
+    uint32_t* __restrict__ mem_start_next, uint32_t* __restrict__ mem_leaf_next) {
     __shared__ uint32_t s_scan[40];
     const uint32_t per = (n_tiles + blockDim.x - 1) / blockDim.x;
     const uint32_t t0 = threadIdx.x * per;
@@ -972,14 +1083,13 @@ __global__ void __launch_bounds__(1024) part_scan_kernel(
     __syncthreads();
     const uint32_t Q = 1u << level;
     for (uint32_t q = threadIdx.x; q < Q; q += blockDim.x) {
-        uint32_t cnt = seg_cnt[q];
+        const uint32_t cnt = seg_cnt[q];
         uint32_t ts = 0, tt = 0;
         if (cnt > 0) {
             ts = blk_true[seg_start_blk[q]] + seg_start_part[q];
-            uint32_t te = blk_true[seg_end_blk[q]] + seg_end_part[q];
-            tt = te - ts;
+            tt = blk_true[seg_end_blk[q]] + seg_end_part[q] - ts;
         }
-        uint32_t fc = cnt - tt;
+        const uint32_t fc = cnt - tt;
         t_start[q] = ts;
         f_cnt[q] = fc;
         child_cnt[q] = fc;
@@ -989,18 +1099,31 @@ __global__ void __launch_bounds__(1024) part_scan_kernel(
         seg_off_next[q + Q] = seg_off[q] + fc;
         seg_cnt_next[q + Q] = tt;
     }
+    // each segment splits in place into (false child, true child)
+    for (uint32_t k = threadIdx.x; k < Q; k += blockDim.x) {
+        const uint32_t q = mem_leaf[k];
+        const uint32_t cnt = seg_cnt[q];
+        uint32_t tt = 0;
+        if (cnt > 0)
+            tt = blk_true[seg_end_blk[q]] + seg_end_part[q] - (blk_true[seg_start_blk[q]] + seg_start_part[q]);
+        mem_leaf_next[2 * k] = q;
+        mem_start_next[2 * k] = seg_off[q];
+        mem_leaf_next[2 * k + 1] = q + Q;
+        mem_start_next[2 * k + 1] = seg_off[q] + (cnt - tt);
+    }
 }
 
 __global__ void __launch_bounds__(kPartThreads) part_scatter_kernel(
     int level, int64_t n, const uint8_t* __restrict__ bins_fm, int64_t n_stride,
-    const uint32_t* __restrict__ perm, uint32_t* __restrict__ perm_next, uint16_t* __restrict__ leaf,
-    const uint32_t* __restrict__ seg_off, const uint32_t* __restrict__ blk_off,
+    const uint32_t* __restrict__ perm, uint32_t* __restrict__ perm_next,
+    const uint32_t* __restrict__ seg_off, const uint32_t* __restrict__ mem_start,
+    const uint32_t* __restrict__ mem_leaf, const uint32_t* __restrict__ blk_off,
     const uint32_t* __restrict__ t_start, const uint32_t* __restrict__ f_cnt,
     const TreeState* __restrict__ ts) {
     __shared__ uint32_t s_idx[kPartTile];
     __shared__ uint32_t s_scan[40];
     const PartView pv = part_view(ts, level, bins_fm, n_stride);
-    const uint32_t mask = (1u << level) - 1u;
+    const int K = 1 << level;
     const int64_t base = (int64_t)blockIdx.x * kPartTile;
     for (int k = threadIdx.x; k < kPartTile; k += blockDim.x) {
         int64_t j = base + k;
@@ -1008,60 +1131,44 @@ __global__ void __launch_bounds__(kPartThreads) part_scatter_kernel(
     }
     __syncthreads();
     const int k0 = threadIdx.x * kPartItems;
+    const int64_t j0 = base + k0;
+    const int cnt_items = j0 >= n ? 0 : (int)(n - j0 < kPartItems ? n - j0 : kPartItems);
     uint32_t flags = 0;
     int cnt = 0;
-#pragma unroll
-    for (int u = 0; u < kPartItems; ++u) {
-        uint32_t i = s_idx[k0 + u];
-        if (i != 0xffffffffu) {
-            uint32_t fl = (int32_t)pv.col[i] > pv.bin;
-            flags |= fl << u;
-            cnt += fl;
-        }
+    for (int u = 0; u < cnt_items; ++u) {
+        const uint32_t fl = (int32_t)pv.col[s_idx[k0 + u]] > pv.bin;
+        flags |= fl << u;
+        cnt += fl;
     }
-    uint32_t excl = block_excl_scan<uint32_t>((uint32_t)cnt, s_scan, nullptr);
+    const uint32_t excl = block_excl_scan<uint32_t>((uint32_t)cnt, s_scan, nullptr);
+    if (cnt_items == 0) return;
     uint32_t T = blk_off[blockIdx.x] + excl;
-#pragma unroll
-    for (int u = 0; u < kPartItems; ++u) {
-        uint32_t i = s_idx[k0 + u];
-        if (i == 0xffffffffu) break;
-        uint32_t j = (uint32_t)(base + k0 + u);
-        uint32_t q = level ? (leaf[i] & mask) : 0u;
-        uint32_t fl = (flags >> u) & 1u;
-        uint32_t rel = T - t_start[q];
-        uint32_t dest = fl ? seg_off[q] + f_cnt[q] + rel : j - rel;
-        perm_next[dest] = i;
-        leaf[i] = (uint16_t)(q | (fl << level));
+    walk_segments(mem_start, K, (uint32_t)j0, cnt_items, [&](int u, uint32_t j, int k) {
+        const uint32_t q = mem_leaf[k];
+        const uint32_t fl = (flags >> u) & 1u;
+        const uint32_t rel = T - t_start[q];
+        const uint32_t dest = fl ? seg_off[q] + f_cnt[q] + rel : j - rel;
+        perm_next[dest] = s_idx[k0 + u];
         T += fl;
-    }
+    });
 }
 
 void launch_partition(int level, int64_t n, const uint8_t* bins_fm, int64_t n_stride,
-                      const uint32_t* perm, uint32_t* perm_next, uint16_t* leaf, uint32_t* seg_off,
-                      uint32_t* seg_cnt, uint32_t* scratch, uint32_t* seg_start_blk,
-                      uint32_t* seg_start_part, uint32_t* blk_true, uint32_t* child_cnt,
-                      TreeState* ts, cudaStream_t st) {
-    // scratch layout: [seg_end_blk | seg_end_part | t_start | f_cnt | seg_off_next | seg_cnt_next]
-    const uint32_t Qmax = 1u << 16;
-    uint32_t* seg_end_blk = scratch;
-    uint32_t* seg_end_part = scratch + Qmax;
-    uint32_t* t_start = scratch + 2 * Qmax;
-    uint32_t* f_cnt = scratch + 3 * Qmax;
-    uint32_t* seg_off_next = scratch + 4 * Qmax;
-    uint32_t* seg_cnt_next = scratch + 6 * Qmax;
+                      const uint32_t* perm, uint32_t* perm_next, SegTables& sg, uint32_t* blk_true,
+                      uint32_t* child_cnt, TreeState* ts, cudaStream_t st) {
     const uint32_t tiles = (uint32_t)((n + kPartTile - 1) / kPartTile);
     if (tiles == 0) return;
-    part_count_kernel<<<tiles, kPartThreads, 0, st>>>(level, n, bins_fm, n_stride, perm, leaf,
-                                                       seg_start_blk, seg_start_part, seg_end_blk,
-                                                       seg_end_part, blk_true, ts);
-    part_scan_kernel<<<1, 1024, 0, st>>>(level, tiles, blk_true, seg_off, seg_cnt, seg_start_blk,
-                                         seg_start_part, seg_end_blk, seg_end_part, t_start, f_cnt,
-                                         child_cnt, seg_off_next, seg_cnt_next);
+    part_count_kernel<<<tiles, kPartThreads, 0, st>>>(level, n, bins_fm, n_stride, perm, sg.seg_cnt,
+                                                       sg.mem_start, sg.mem_leaf, sg.start_blk,
+                                                       sg.start_part, sg.end_blk, sg.end_part, blk_true, ts);
+    part_scan_kernel<<<1, 1024, 0, st>>>(level, tiles, blk_true, sg.seg_off, sg.seg_cnt, sg.mem_leaf,
+                                         sg.start_blk, sg.start_part, sg.end_blk, sg.end_part, sg.t_start,
+                                         sg.f_cnt, child_cnt, sg.seg_off_next, sg.seg_cnt_next,
+                                         sg.mem_start_next, sg.mem_leaf_next);
     part_scatter_kernel<<<tiles, kPartThreads, 0, st>>>(level, n, bins_fm, n_stride, perm, perm_next,
-                                                         leaf, seg_off, blk_true, t_start, f_cnt, ts);
-    const uint32_t Qn = 2u << level;
-    cudaMemcpyAsync(seg_off, seg_off_next, sizeof(uint32_t) * Qn, cudaMemcpyDeviceToDevice, st);
-    cudaMemcpyAsync(seg_cnt, seg_cnt_next, sizeof(uint32_t) * Qn, cudaMemcpyDeviceToDevice, st);
+                                                         sg.seg_off, sg.mem_start, sg.mem_leaf, blk_true,
+                                                         sg.t_start, sg.f_cnt, ts);
+    sg.swap();
 }
 
 // small_side[q] = 1 when the TRUE child of q is the one to build (<= rows, as
@@ -1081,13 +1188,32 @@ void launch_small_side(int level_next, const uint32_t* child_cnt_global, uint8_t
 }
 
 // ============================================================================
-// last level: route + unsampled leaf sums (boosting.rs:2470-2517 Gradient
-// leaves over the full w*der1 / w channels), exact int64.
+// last level: final leaf id of every row (natural order), then the unsampled
+// leaf sums (boosting.rs:2470-2517 Gradient leaves over the full w*der1 / w
+// channels) as exact int64 sums.
 // ============================================================================
-__global__ void __launch_bounds__(256) route_leafsum_kernel(
+__global__ void __launch_bounds__(kPartThreads) route_final_kernel(
     int level, int64_t n, const uint8_t* __restrict__ bins_fm, int64_t n_stride,
-    uint16_t* __restrict__ leaf, const double* __restrict__ wd1, const double* __restrict__ weight,
-    int depth, const TreeState* __restrict__ ts, ull* __restrict__ leaf_sums) {
+    const uint32_t* __restrict__ perm, const uint32_t* __restrict__ mem_start,
+    const uint32_t* __restrict__ mem_leaf, uint16_t* __restrict__ leaf,
+    const TreeState* __restrict__ ts) {
+    const PartView pv = part_view(ts, level, bins_fm, n_stride);
+    const int K = 1 << level;
+    const int64_t j0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * kPartItems;
+    if (j0 >= n) return;
+    const int cnt = (int)(n - j0 < kPartItems ? n - j0 : kPartItems);
+    walk_segments(mem_start, K, (uint32_t)j0, cnt, [&](int, uint32_t j, int k) {
+        const uint32_t i = perm ? perm[j] : j;
+        const uint32_t fl = (int32_t)pv.col[i] > pv.bin;
+        leaf[i] = (uint16_t)(mem_leaf[k] | (fl << level));
+    });
+}
+
+__global__ void __launch_bounds__(256) leafsum_kernel(int64_t n, const uint16_t* __restrict__ leaf,
+                                                      const double* __restrict__ wd1,
+                                                      const double* __restrict__ weight, int depth,
+                                                      const TreeState* __restrict__ ts,
+                                                      ull* __restrict__ leaf_sums) {
     extern __shared__ ull lsm[];
     const int L = 1 << depth;
     const bool use_smem = depth <= 10;
@@ -1095,14 +1221,11 @@ __global__ void __launch_bounds__(256) route_leafsum_kernel(
         for (int k = threadIdx.x; k < 2 * L; k += blockDim.x) lsm[k] = 0ull;
         __syncthreads();
     }
-    const PartView pv = part_view(ts, level, bins_fm, n_stride);
-    const uint32_t mask = (1u << level) - 1u;
     const double sd = ts->sc.scale[2], sw = ts->sc.scale[3];
     ull* acc = use_smem ? lsm : leaf_sums;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
          i += (int64_t)gridDim.x * blockDim.x) {
-        uint32_t q = (level ? (leaf[i] & mask) : 0u) | ((uint32_t)((int32_t)pv.col[i] > pv.bin) << level);
-        leaf[i] = (uint16_t)q;
+        const uint32_t q = leaf[i];
         const double w = weight ? weight[i] : 1.0;
         atomicAdd(acc + 2 * q, (ull)__double2ll_rn(__dmul_rn(wd1[i], sd)));
         atomicAdd(acc + 2 * q + 1, (ull)__double2ll_rn(__dmul_rn(w, sw)));
@@ -1115,14 +1238,17 @@ __global__ void __launch_bounds__(256) route_leafsum_kernel(
 }
 
 void launch_route_leafsum(int level, int64_t n, const uint8_t* bins_fm, int64_t n_stride,
-                          uint16_t* leaf, const double* wd1, const double* weight, int depth,
-                          TreeState* ts, ull* leaf_sums, cudaStream_t st) {
+                          const uint32_t* perm, const SegTables& sg, uint16_t* leaf, const double* wd1,
+                          const double* weight, int depth, TreeState* ts, ull* leaf_sums,
+                          cudaStream_t st) {
+    if (n <= 0) return;
+    const int64_t threads = (n + kPartItems - 1) / kPartItems;
+    route_final_kernel<<<(unsigned)((threads + kPartThreads - 1) / kPartThreads), kPartThreads, 0, st>>>(
+        level, n, bins_fm, n_stride, perm, sg.mem_start, sg.mem_leaf, leaf, ts);
     int64_t blocks = (n + 255) / 256;
     if (blocks > 148 * 4) blocks = 148 * 4;
-    if (blocks < 1) blocks = 1;
-    size_t smem = depth <= 10 ? sizeof(ull) * 2 * (1 << depth) : 0;
-    route_leafsum_kernel<<<(unsigned)blocks, 256, smem, st>>>(level, n, bins_fm, n_stride, leaf, wd1,
-                                                               weight, depth, ts, leaf_sums);
+    const size_t smem = depth <= 10 ? sizeof(ull) * 2 * (1 << depth) : 0;
+    leafsum_kernel<<<(unsigned)blocks, 256, smem, st>>>(n, leaf, wd1, weight, depth, ts, leaf_sums);
 }
 
 // Gradient leaf delta calc_average(sum w*der1, sum w, scaled_l2) (leaf.rs:161-199),

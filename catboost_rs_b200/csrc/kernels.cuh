@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cstdint>
+#include <utility>
 #include <cuda_runtime.h>
 
 #include "cbgpu_common.cuh"
@@ -46,11 +47,33 @@ struct TreeState {
 
 constexpr int kTile = 32;          // features per histogram tile (one per lane)
 constexpr int kHistThreads = 256;  // 8 warps
-constexpr int kChunkRows = 8192;   // rows per histogram work item
+constexpr int kHistStages = 3;     // cp.async ring depth per warp (groups of 32 rows)
+constexpr int kChunkRows = 16384;  // rows per histogram work item
+// Score-channel fixed point: |row value| <= 2^kPackBits, split at bit kPackSplit
+// into (lo, hi) u32 parts whose sums over kChunkRows rows stay below 2^31.
+constexpr int kPackBits = 33;
+constexpr int kPackSplit = 17;
+static_assert((long long)kChunkRows << kPackSplit <= (1ll << 31), "lo sums must fit 31 bits");
+static_assert((long long)kChunkRows << (kPackBits - kPackSplit) <= (1ll << 31), "hi sums must fit 31 bits");
 constexpr int kPartThreads = 256;
 constexpr int kPartItems = 16;     // positions per thread in the partition kernels
 constexpr int kPartTile = kPartThreads * kPartItems;
 constexpr int kBootRun = 8;        // consecutive rows per thread in the bootstrap kernel
+
+// Leaf segments of the leaf-sorted row order: by leaf id (off, cnt) and in
+// position order (mem_start, mem_leaf); *_next are written by the partition
+// and swapped in afterwards.  start/end_* and t_start/f_cnt are P1/P2 scratch.
+struct SegTables {
+    uint32_t *seg_off, *seg_cnt, *mem_start, *mem_leaf;
+    uint32_t *seg_off_next, *seg_cnt_next, *mem_start_next, *mem_leaf_next;
+    uint32_t *start_blk, *start_part, *end_blk, *end_part, *t_start, *f_cnt;
+    void swap() {
+        std::swap(seg_off, seg_off_next);
+        std::swap(seg_cnt, seg_cnt_next);
+        std::swap(mem_start, mem_start_next);
+        std::swap(mem_leaf, mem_leaf_next);
+    }
+};
 
 // ---- begin: quantization / layout ------------------------------------------
 void launch_quantize_column(const float* col, int64_t n, const double* borders, int32_t nb,
@@ -72,41 +95,39 @@ void launch_mvs(int64_t n, int64_t row_offset, const double* wd1, double lambda,
 // s_mode: 0 = none (weights 1), 1 = f32 device sample, 2 = f64 host sample
 void launch_der(int64_t n, int loss, double* approx, const double* target, const double* weight,
                 const uint16_t* leaf, const double* pending_lrv, int s_mode, const float* sw32,
-                const double* sw64, double* wd1, double2* stats, TreeState* ts, bool defer_stats,
-                cudaStream_t st);
-void launch_stats_from_sample(int64_t n, const double* wd1, const double* weight, const float* sw32,
-                              double2* stats, TreeState* ts, cudaStream_t st);
+                const double* sw64, double* wd1, TreeState* ts, bool defer_gh, cudaStream_t st);
+void launch_max_gh(int64_t n, const double* wd1, const double* weight, const float* sw32, TreeState* ts,
+                   cudaStream_t st);
 void launch_scales(TreeState* ts, int64_t n_total, cudaStream_t st);
+void launch_pack_stats(int64_t n, const double* wd1, const double* weight, int s_mode, const float* sw32,
+                       const double* sw64, const TreeState* ts, uint4* qstats, cudaStream_t st);
 void launch_apply(int64_t n, double* approx, const uint16_t* leaf, const double* lrv,
                   cudaStream_t st);
 
 // ---- per level ---------------------------------------------------------------
 void launch_zero(void* p, size_t bytes, cudaStream_t st);
-void launch_hist(const uint8_t* bins_rm, int32_t F_pad, int32_t F, int32_t B,
-                 const double2* stats, const uint32_t* perm, const HistChunk* chunks,
-                 const uint32_t* n_chunks, uint32_t max_chunks, const TreeState* ts, ull* built,
-                 cudaStream_t st);
-// level 0 also initialises the single all-rows segment (seg_off[0] = 0, seg_cnt[0] = n).
-void launch_make_chunks(int level, uint32_t* seg_off, uint32_t* seg_cnt,
-                        const uint8_t* small_side, int64_t n_level0, HistChunk* chunks,
-                        uint32_t* n_chunks, TreeState* ts, cudaStream_t st);
+void launch_hist(const uint8_t* bins_rm, int32_t F_pad, int32_t F, int32_t B, const uint4* qstats,
+                 const uint32_t* perm, const HistChunk* chunks, const uint32_t* n_chunks,
+                 uint32_t max_chunks, ull* built, cudaStream_t st);
+// level 0 also initialises the segment tables to the single all-rows segment.
+void launch_make_chunks(int level, uint32_t* seg_off, uint32_t* seg_cnt, uint32_t* mem_start,
+                        uint32_t* mem_leaf, const uint8_t* small_side, int64_t n_level0,
+                        HistChunk* chunks, uint32_t* n_chunks, TreeState* ts, cudaStream_t st);
 void launch_derive_prefix(int level, int32_t F, int32_t B, const ull* built, const ull* prev,
                           ull* cur, const uint8_t* small_side, cudaStream_t st);
 void launch_score(int level, int32_t F, int32_t B, const ull* cur, const int32_t* border_counts,
                   double l2, int score_fn, double* feat_score, int32_t* feat_bin, TreeState* ts,
                   cudaStream_t st);
-// scratch: 8 * 65536 uint32; seg_start_*: 65536 each; blk_true: ceil(n / kPartTile);
-// child_cnt: 2^(level+1) (false counts, then true counts).
+// blk_true: ceil(n / kPartTile) + 1; child_cnt: 2^(level+1) (false counts, then true).
 void launch_partition(int level, int64_t n, const uint8_t* bins_fm, int64_t n_stride,
-                      const uint32_t* perm, uint32_t* perm_next, uint16_t* leaf, uint32_t* seg_off,
-                      uint32_t* seg_cnt, uint32_t* scratch, uint32_t* seg_start_blk,
-                      uint32_t* seg_start_part, uint32_t* blk_true, uint32_t* child_cnt,
-                      TreeState* ts, cudaStream_t st);
+                      const uint32_t* perm, uint32_t* perm_next, SegTables& sg, uint32_t* blk_true,
+                      uint32_t* child_cnt, TreeState* ts, cudaStream_t st);
 void launch_small_side(int level_next, const uint32_t* child_cnt_global, uint8_t* small_side,
                        cudaStream_t st);
-void launch_route_leafsum(int level, int64_t n, const uint8_t* bins_fm, int64_t n_stride, uint16_t* leaf,
-                          const double* wd1, const double* weight, int depth, TreeState* ts,
-                          ull* leaf_sums, cudaStream_t st);
+void launch_route_leafsum(int level, int64_t n, const uint8_t* bins_fm, int64_t n_stride,
+                          const uint32_t* perm, const SegTables& sg, uint16_t* leaf, const double* wd1,
+                          const double* weight, int depth, TreeState* ts, ull* leaf_sums,
+                          cudaStream_t st);
 void launch_leaf_values(int depth, int n_splits_expected, const ull* leaf_sums, double l2, double lr,
                         TreeState* ts, double* leaf_raw, double* leaf_lrv, cudaStream_t st);
 void launch_leaf_export(int64_t n, const uint16_t* leaf, void* out, int bytes, cudaStream_t st);

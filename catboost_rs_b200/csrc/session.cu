@@ -127,17 +127,14 @@ struct cbgpu_session {
     double* weight = nullptr;
     double* approx = nullptr;
     double* wd1 = nullptr;
-    double2* stats = nullptr;
+    uint4* qstats = nullptr;      // per-row packed fixed-point (g_lo, g_hi, h_lo, h_hi)
     float* sw32 = nullptr;
     double* sw64 = nullptr;
     double* mvs_thr = nullptr;
     uint16_t* leaf = nullptr;
     uint32_t* perm[2] = {nullptr, nullptr};
-    uint32_t* seg_off = nullptr;
-    uint32_t* seg_cnt = nullptr;
-    uint32_t* part_scratch = nullptr;
-    uint32_t* seg_start_blk = nullptr;
-    uint32_t* seg_start_part = nullptr;
+    uint32_t* seg_mem = nullptr;  // backing store of the segment tables
+    SegTables sg{};
     uint32_t* blk_true = nullptr;
     uint32_t* child_cnt = nullptr;
     uint8_t* small_side = nullptr;
@@ -240,18 +237,23 @@ int alloc_session(cbgpu_session* s, const cbgpu_begin_args* a) {
     if (s->weighted) DA(s->weight, n);
     DA(s->approx, n);
     DA(s->wd1, n);
-    DA(s->stats, n);
+    DA(s->qstats, n);
     DA(s->sw32, n);
     if (s->sample_from_host) DA(s->sw64, n);
     DA(s->mvs_thr, (n + 8191) / 8192);
     DA(s->leaf, n);
     DA(s->perm[0], n);
     DA(s->perm[1], n);
-    DA(s->seg_off, 1 << 16);
-    DA(s->seg_cnt, 1 << 16);
-    DA(s->part_scratch, 8u << 16);
-    DA(s->seg_start_blk, 1 << 16);
-    DA(s->seg_start_part, 1 << 16);
+    {
+        const size_t Q = (size_t)1 << 16;  // up to 2^15 leaves before the last split, 2^16 after
+        DA(s->seg_mem, 14 * Q);
+        uint32_t* p = s->seg_mem;
+        uint32_t** tabs[14] = {&s->sg.seg_off, &s->sg.seg_cnt, &s->sg.mem_start, &s->sg.mem_leaf,
+                               &s->sg.seg_off_next, &s->sg.seg_cnt_next, &s->sg.mem_start_next,
+                               &s->sg.mem_leaf_next, &s->sg.start_blk, &s->sg.start_part,
+                               &s->sg.end_blk, &s->sg.end_part, &s->sg.t_start, &s->sg.f_cnt};
+        for (int k = 0; k < 14; ++k) *tabs[k] = p + (size_t)k * Q;
+    }
     DA(s->blk_true, (n + kPartTile - 1) / kPartTile + 1);
     DA(s->child_cnt, 1 << 17);
     DA(s->small_side, 1 << 16);
@@ -299,9 +301,8 @@ void free_session(cbgpu_session* s) {
     cudaSetDevice(s->device);
     if (s->st) cudaStreamSynchronize(s->st);
     void* ptrs[] = {s->bins_rm, s->bins_fm, s->d_border_counts, s->target, s->weight, s->approx,
-                    s->wd1, s->stats, s->sw32, s->sw64, s->mvs_thr, s->leaf, s->perm[0], s->perm[1],
-                    s->seg_off, s->seg_cnt, s->part_scratch, s->seg_start_blk, s->seg_start_part,
-                    s->blk_true, s->child_cnt, s->small_side, s->chunks, s->n_chunks, s->built,
+                    s->wd1, s->qstats, s->sw32, s->sw64, s->mvs_thr, s->leaf, s->perm[0], s->perm[1],
+                    s->seg_mem, s->blk_true, s->child_cnt, s->small_side, s->chunks, s->n_chunks, s->built,
                     s->hist[0], s->hist[1], s->feat_score, s->feat_bin, s->leaf_sums, s->leaf_raw,
                     s->leaf_lrv, s->ts, s->d_err, s->leaf_export};
     for (void* p : ptrs)
@@ -479,13 +480,13 @@ int grow(cbgpu_session* s, const double* approx_h, const double* target_h, int64
         }
     }
     launch_der(s->n, s->loss, s->approx, s->target, s->weight, s->leaf, s->pending ? s->leaf_lrv : nullptr,
-               s_mode, s->sw32, s->sw64, s->wd1, s->stats, s->ts, mvs, st);
+               s_mode, s->sw32, s->sw64, s->wd1, s->ts, mvs, st);
     ++launches;
     s->pending = false;
     if (mvs) {
         launch_mvs(s->n, s->row_offset, s->wd1, mvs_lam, (double)s->sample_rate, mvs_seed, nullptr,
                    s->mvs_thr, s->sw32, st);
-        launch_stats_from_sample(s->n, s->wd1, s->weight, s->sw32, s->stats, s->ts, st);
+        launch_max_gh(s->n, s->wd1, s->weight, s->sw32, s->ts, st);
         launches += 3;
     }
     {
@@ -494,7 +495,8 @@ int grow(cbgpu_session* s, const double* approx_h, const double* target_h, int64
         if (rc) return rc;
     }
     launch_scales(s->ts, s->n_total, st);
-    ++launches;
+    launch_pack_stats(s->n, s->wd1, s->weight, s_mode, s->sw32, s->sw64, s->ts, s->qstats, st);
+    launches += 2;
     rec(1);
 
     // ---- level loop
@@ -507,11 +509,11 @@ int grow(cbgpu_session* s, const double* approx_h, const double* target_h, int64
         CU(cudaMemsetAsync(s->built, 0, sizeof(ull) * built_slots * row_cells, st));
         const uint32_t max_chunks =
             (uint32_t)(s->n / kChunkRows + (l == 0 ? 1 : (1u << (l - 1))) + 1);
-        launch_make_chunks(l, s->seg_off, s->seg_cnt, l ? s->small_side : nullptr, s->n, s->chunks,
-                           s->n_chunks, s->ts, st);
+        launch_make_chunks(l, s->sg.seg_off, s->sg.seg_cnt, s->sg.mem_start, s->sg.mem_leaf,
+                           l ? s->small_side : nullptr, s->n, s->chunks, s->n_chunks, s->ts, st);
         rec(e);
-        launch_hist(s->bins_rm, s->F_pad, s->F, s->B, s->stats, l == 0 ? nullptr : s->perm[pp], s->chunks,
-                    s->n_chunks, max_chunks, s->ts, s->built, st);
+        launch_hist(s->bins_rm, s->F_pad, s->F, s->B, s->qstats, l == 0 ? nullptr : s->perm[pp], s->chunks,
+                    s->n_chunks, max_chunks, s->built, st);
         rec(e + 1);
         launches += 2;
         {
@@ -526,8 +528,7 @@ int grow(cbgpu_session* s, const double* approx_h, const double* target_h, int64
         rec(e + 3);
         if (l + 1 < D) {
             launch_partition(l, s->n, s->bins_fm, s->n_stride, l == 0 ? nullptr : s->perm[pp],
-                             s->perm[pp ^ 1], s->leaf, s->seg_off, s->seg_cnt, s->part_scratch,
-                             s->seg_start_blk, s->seg_start_part, s->blk_true, s->child_cnt, s->ts, st);
+                             s->perm[pp ^ 1], s->sg, s->blk_true, s->child_cnt, s->ts, st);
             pp ^= 1;
             rec(e + 4);
             int rc = allreduce(s, s->child_cnt, (size_t)2 << l, ncclUint32, ncclSum);
@@ -536,9 +537,9 @@ int grow(cbgpu_session* s, const double* approx_h, const double* target_h, int64
             launches += 4;
         } else {
             CU(cudaMemsetAsync(s->leaf_sums, 0, sizeof(ull) * 2 * L, st));
-            launch_route_leafsum(l, s->n, s->bins_fm, s->n_stride, s->leaf, s->wd1, s->weight, D, s->ts,
-                                 s->leaf_sums, st);
-            ++launches;
+            launch_route_leafsum(l, s->n, s->bins_fm, s->n_stride, l == 0 ? nullptr : s->perm[pp], s->sg,
+                                 s->leaf, s->wd1, s->weight, D, s->ts, s->leaf_sums, st);
+            launches += 2;
             rec(e + 4);
             int rc = allreduce(s, s->leaf_sums, (size_t)2 * L, ncclUint64, ncclSum);
             if (rc) return rc;
@@ -759,9 +760,7 @@ int cbgpu_session_bins(cbgpu_session* s, uint8_t* out, int64_t n, int32_t F) {
 int cbgpu_session_last_sample(cbgpu_session* s, double* out, int64_t n) {
     if (!s || !out || n != s->n) return fail(CBGPU_ERR_INVALID, "bad arguments");
     CU(cudaSetDevice(s->device));
-    std::vector<double2> st((size_t)n);
-    std::vector<double> wd((size_t)n);
-    CU(cudaMemcpy(st.data(), s->stats, sizeof(double2) * n, cudaMemcpyDeviceToHost));
+    CU(cudaStreamSynchronize(s->st));
     if (s->sample_from_host) {
         CU(cudaMemcpy(out, s->sw64, sizeof(double) * n, cudaMemcpyDeviceToHost));
         return CBGPU_OK;
@@ -839,16 +838,21 @@ int cbgpu_compute_gradients(int32_t loss, const double* approx, const double* ta
 
 int cbgpu_histogram(const uint8_t* bins_rm_h, int64_t n, int32_t F, int32_t B, const double* g,
                     const double* h, const int32_t* leaf_of, int32_t n_leaves, double* out_hist) {
-    if (n < 0 || F < 1 || B < 1 || B > 256 || n_leaves < 1 || !out_hist || (n > 0 && (!bins_rm_h || !g || !h)))
+    if (n < 0 || F < 1 || B < 1 || B > 256 || n_leaves < 1 || !out_hist ||
+        (n > 0 && (!bins_rm_h || !g || !h)))
         return fail(CBGPU_ERR_INVALID, "bad arguments");
+    for (int64_t i = 0; i < n; ++i)
+        for (int f = 0; f < F; ++f)
+            if (bins_rm_h[(size_t)i * F + f] >= B)
+                return fail(CBGPU_ERR_INVALID, "bin %d >= n_bins %d at row %lld feature %d",
+                            bins_rm_h[(size_t)i * F + f], B, (long long)i, f);
     int ndev = 0;
     if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0)
         return fail(CBGPU_ERR_NO_DEVICE, "no CUDA device");
     const int F_pad = (int)round_up(F, 32);
-    // host: stable counting sort of rows by leaf -> one contiguous segment per leaf
+    // stable counting sort of rows by leaf -> one contiguous segment per leaf
     std::vector<uint32_t> perm;
     std::vector<HistChunk> chunks;
-    perm.reserve((size_t)n);
     {
         std::vector<int64_t> cnt((size_t)n_leaves + 1, 0);
         for (int64_t i = 0; i < n; ++i) {
@@ -869,65 +873,56 @@ int cbgpu_histogram(const uint8_t* bins_rm_h, int64_t n, int32_t F, int32_t B, c
     }
     std::vector<uint8_t> rm((size_t)std::max<int64_t>(n, 1) * F_pad, 0);
     for (int64_t i = 0; i < n; ++i) memcpy(&rm[(size_t)i * F_pad], bins_rm_h + (size_t)i * F, (size_t)F);
-    // the scales: max |g|, |h| over the rows, as the session derives them
-    double mg = 0.0, mh = 0.0;
-    for (int64_t i = 0; i < n; ++i) {
-        mg = std::max(mg, std::fabs(g[i]));
-        mh = std::max(mh, std::fabs(h[i]));
-    }
-    TreeState hts{};
-    double mx[2] = {mg, mh};
-    for (int c = 0; c < 2; ++c) {
-        int s = 0;
-        if (mx[c] > 0.0) {
-            int e;
-            std::frexp(mx[c] * (double)std::max<int64_t>(n, 1), &e);
-            s = 62 - e;
+    // the session's scale rule for the score channels (max |v| * 2^s < 2^kPackBits)
+    double scale[2], inv[2];
+    {
+        double mx[2] = {0.0, 0.0};
+        for (int64_t i = 0; i < n; ++i) {
+            mx[0] = std::max(mx[0], std::fabs(g[i]));
+            mx[1] = std::max(mx[1], std::fabs(h[i]));
         }
-        hts.sc.scale[c] = std::ldexp(1.0, s);
-        hts.sc.inv[c] = std::ldexp(1.0, -s);
+        for (int c = 0; c < 2; ++c) {
+            int sx = 0;
+            if (mx[c] > 0.0) {
+                int e;
+                std::frexp(mx[c], &e);
+                sx = kPackBits - e;
+            }
+            scale[c] = std::ldexp(1.0, sx);
+            inv[c] = std::ldexp(1.0, -sx);
+        }
+    }
+    std::vector<uint4> qs((size_t)std::max<int64_t>(n, 1));
+    for (int64_t i = 0; i < n; ++i) {
+        long long qg = std::llrint(g[i] * scale[0]), qh = std::llrint(h[i] * scale[1]);
+        qs[(size_t)i] = make_uint4((uint32_t)(qg & ((1ll << kPackSplit) - 1)), (uint32_t)(int32_t)(qg >> kPackSplit),
+                                   (uint32_t)(qh & ((1ll << kPackSplit) - 1)), (uint32_t)(int32_t)(qh >> kPackSplit));
     }
     uint8_t* d_rm;
-    double2* d_st;
+    uint4* d_qs;
     uint32_t *d_perm, *d_nch;
     HistChunk* d_ch;
-    TreeState* d_ts;
     ull* d_out;
     const size_t cells = (size_t)n_leaves * F * B * 2;
     DA(d_rm, rm.size());
-    DA(d_st, (size_t)std::max<int64_t>(n, 1));
+    DA(d_qs, qs.size());
     DA(d_perm, std::max<size_t>(perm.size(), 1));
     DA(d_ch, std::max<size_t>(chunks.size(), 1));
     DA(d_nch, 1);
-    DA(d_ts, 1);
     DA(d_out, cells);
-    std::vector<double2> st((size_t)n);
-    for (int64_t i = 0; i < n; ++i) st[(size_t)i] = make_double2(g[i], h[i]);
     uint32_t nch = (uint32_t)chunks.size();
     CU(cudaMemcpy(d_rm, rm.data(), rm.size(), cudaMemcpyHostToDevice));
-    if (n > 0) CU(cudaMemcpy(d_st, st.data(), sizeof(double2) * n, cudaMemcpyHostToDevice));
+    CU(cudaMemcpy(d_qs, qs.data(), sizeof(uint4) * qs.size(), cudaMemcpyHostToDevice));
     if (!perm.empty()) CU(cudaMemcpy(d_perm, perm.data(), sizeof(uint32_t) * perm.size(), cudaMemcpyHostToDevice));
     if (!chunks.empty()) CU(cudaMemcpy(d_ch, chunks.data(), sizeof(HistChunk) * chunks.size(), cudaMemcpyHostToDevice));
     CU(cudaMemcpy(d_nch, &nch, sizeof(uint32_t), cudaMemcpyHostToDevice));
-    CU(cudaMemcpy(d_ts, &hts, sizeof(TreeState), cudaMemcpyHostToDevice));
     CU(cudaMemset(d_out, 0, sizeof(ull) * cells));
-    // bin range check on the host (the device kernel trusts its inputs)
-    for (int64_t i = 0; i < n; ++i)
-        for (int f = 0; f < F; ++f)
-            if (bins_rm_h[(size_t)i * F + f] >= B) {
-                cudaFree(d_rm); cudaFree(d_st); cudaFree(d_perm); cudaFree(d_ch); cudaFree(d_nch);
-                cudaFree(d_ts); cudaFree(d_out);
-                return fail(CBGPU_ERR_INVALID, "bin %d >= n_bins %d at row %lld feature %d",
-                            bins_rm_h[(size_t)i * F + f], B, (long long)i, f);
-            }
-    launch_hist(d_rm, F_pad, F, B, d_st, d_perm, d_ch, d_nch, std::max<uint32_t>(nch, 1), d_ts, d_out, 0);
+    launch_hist(d_rm, F_pad, F, B, d_qs, d_perm, d_ch, d_nch, std::max<uint32_t>(nch, 1), d_out, 0);
     CU(cudaGetLastError());
     std::vector<ull> hout(cells);
     CU(cudaMemcpy(hout.data(), d_out, sizeof(ull) * cells, cudaMemcpyDeviceToHost));
-    for (size_t k = 0; k < cells; ++k)
-        out_hist[k] = (double)(long long)hout[k] * hts.sc.inv[k & 1];
-    cudaFree(d_rm); cudaFree(d_st); cudaFree(d_perm); cudaFree(d_ch); cudaFree(d_nch);
-    cudaFree(d_ts); cudaFree(d_out);
+    for (size_t k = 0; k < cells; ++k) out_hist[k] = (double)(long long)hout[k] * inv[k & 1];
+    cudaFree(d_rm); cudaFree(d_qs); cudaFree(d_perm); cudaFree(d_ch); cudaFree(d_nch); cudaFree(d_out);
     return CBGPU_OK;
 }
 
