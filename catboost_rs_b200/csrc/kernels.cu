@@ -602,23 +602,27 @@ __global__ void __launch_bounds__(kHistThreads, 2) hist_kernel(
     const HistChunk* __restrict__ chunks, const uint32_t* __restrict__ n_chunks,
     ull* __restrict__ built) {
     extern __shared__ __align__(16) uint32_t hs[];  // [B][4][32] then the staging ring
-    if (blockIdx.x >= *n_chunks) return;
-    const HistChunk ck = chunks[blockIdx.x];
-    const int tile = blockIdx.y;
+    // blockIdx.x = feature tile (fastest), so the tiles of one row chunk run
+    // together and share the L2 lines of those rows; blocks stride over chunks
+    // when there are more than gridDim.y.
+    const int tile = blockIdx.x;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     constexpr int kWarps = kHistThreads / 32;
     uint8_t* sbins = (uint8_t*)(hs + B * 128) + (size_t)warp * kHistStages * 32 * 32;
     uint4* sstat = (uint4*)((uint8_t*)(hs + B * 128) + (size_t)kWarps * kHistStages * 32 * 32) +
                    (size_t)warp * kHistStages * 32;
-    for (int k = threadIdx.x; k < B * 128; k += blockDim.x) hs[k] = 0u;
-    __syncthreads();
-
     const int f = tile * kTile + lane;
     const bool active = f < F;
     uint32_t* my = hs + lane;
+    const uint8_t* tile_base = bins_rm + tile * kTile;
+    const uint32_t nch = *n_chunks;
+    for (uint32_t c = blockIdx.y; c < nch; c += gridDim.y) {
+    const HistChunk ck = chunks[c];
+    for (int k = threadIdx.x; k < B * 128; k += blockDim.x) hs[k] = 0u;
+    __syncthreads();
+
     const uint32_t start = ck.start, len = ck.len;
     const uint32_t n_groups = (len + 31) >> 5;
-    const uint8_t* tile_base = bins_rm + tile * kTile;
 
     // groups of this warp: g = warp, warp + kWarps, ...
     auto row_of = [&](uint32_t g) -> uint32_t {  // row index for lane's row of group g (or ~0)
@@ -626,7 +630,7 @@ __global__ void __launch_bounds__(kHistThreads, 2) hist_kernel(
         if (g >= n_groups || r >= len) return 0xffffffffu;
         return kGather ? __ldg(perm + start + r) : start + r;
     };
-    auto issue = [&](uint32_t g, uint32_t i, int st) {
+    auto issue = [&](uint32_t i, int st) {
         if (i != 0xffffffffu) {
             uint8_t* d = sbins + ((size_t)st * 32 + lane) * 32;
             const uint8_t* src = tile_base + (size_t)i * F_pad;
@@ -637,18 +641,16 @@ __global__ void __launch_bounds__(kHistThreads, 2) hist_kernel(
         cp_async_commit();
     };
     uint32_t g = warp;
-    // prologue: stages 0 .. kHistStages-2
     uint32_t inext = row_of(g);
 #pragma unroll
     for (int p = 0; p < kHistStages - 1; ++p) {
-        issue(g + p * kWarps, inext, p);
+        issue(inext, p);
         inext = row_of(g + (p + 1) * kWarps);
     }
     int st = 0;
     for (; g < n_groups; g += kWarps) {
         // keep kHistStages - 1 groups in flight
-        const int st_issue = (st + kHistStages - 1) % kHistStages;
-        issue(g + (kHistStages - 1) * kWarps, inext, st_issue);
+        issue(inext, (st + kHistStages - 1) % kHistStages);
         inext = row_of(g + kHistStages * kWarps);
         cp_async_wait<kHistStages - 1>();
         __syncwarp();
@@ -667,21 +669,21 @@ __global__ void __launch_bounds__(kHistThreads, 2) hist_kernel(
                 }
 #pragma unroll
                 for (int v = 0; v < 4; ++v) {
-                    uint32_t* c = my + b[v] * 128;
-                    atomicAdd(c, s[v].x);
-                    atomicAdd(c + 32, s[v].y);
-                    atomicAdd(c + 64, s[v].z);
-                    atomicAdd(c + 96, s[v].w);
+                    uint32_t* cc = my + b[v] * 128;
+                    atomicAdd(cc, s[v].x);
+                    atomicAdd(cc + 32, s[v].y);
+                    atomicAdd(cc + 64, s[v].z);
+                    atomicAdd(cc + 96, s[v].w);
                 }
             }
             for (; u < cnt; ++u) {
                 const uint32_t bb = sb[u * 32];
                 const uint4 s = ss[u];
-                uint32_t* c = my + bb * 128;
-                atomicAdd(c, s.x);
-                atomicAdd(c + 32, s.y);
-                atomicAdd(c + 64, s.z);
-                atomicAdd(c + 96, s.w);
+                uint32_t* cc = my + bb * 128;
+                atomicAdd(cc, s.x);
+                atomicAdd(cc + 32, s.y);
+                atomicAdd(cc + 64, s.z);
+                atomicAdd(cc + 96, s.w);
             }
         }
         __syncwarp();  // the stage is refilled next iteration
@@ -694,12 +696,14 @@ __global__ void __launch_bounds__(kHistThreads, 2) hist_kernel(
     for (int k = threadIdx.x; k < B * 32; k += blockDim.x) {
         const int b = k >> 5, l = k & 31;
         if (l >= nf) continue;
-        const uint32_t* c = hs + b * 128 + l;
-        const long long gsum = (long long)(int32_t)c[32] * (1ll << kPackSplit) + (long long)c[0];
-        const long long hsum = (long long)(int32_t)c[96] * (1ll << kPackSplit) + (long long)c[64];
+        const uint32_t* cc = hs + b * 128 + l;
+        const long long gsum = (long long)(int32_t)cc[32] * (1ll << kPackSplit) + (long long)cc[0];
+        const long long hsum = (long long)(int32_t)cc[96] * (1ll << kPackSplit) + (long long)cc[64];
         ull* o = out + ((size_t)l * B + b) * 2;
         if (gsum) atomicAdd(o, (ull)gsum);
         if (hsum) atomicAdd(o + 1, (ull)hsum);
+    }
+    __syncthreads();  // the histogram is zeroed again for the next chunk
     }
 }
 
@@ -718,7 +722,7 @@ void launch_hist(const uint8_t* bins_rm, int32_t F_pad, int32_t F, int32_t B, co
         cudaFuncSetAttribute(hist_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
         attr = true;
     }
-    dim3 grid(max_chunks, (unsigned)((F + kTile - 1) / kTile));
+    dim3 grid((unsigned)((F + kTile - 1) / kTile), max_chunks < 65535u ? max_chunks : 65535u);
     if (perm)
         hist_kernel<true><<<grid, kHistThreads, smem, st>>>(bins_rm, F_pad, F, B, qstats, perm, chunks,
                                                              n_chunks, built);
@@ -1030,10 +1034,15 @@ __global__ void __launch_bounds__(kPartThreads) part_count_kernel(
     const int k0 = threadIdx.x * kPartItems;
     const int64_t j0 = base + k0;
     const int cnt_items = j0 >= n ? 0 : (int)(n - j0 < kPartItems ? n - j0 : kPartItems);
+    // all item loads issued before any is consumed (memory-level parallelism)
+    uint32_t bins_u[kPartItems];
+#pragma unroll
+    for (int u = 0; u < kPartItems; ++u) bins_u[u] = u < cnt_items ? (uint32_t)__ldg(pv.col + s_idx[k0 + u]) : 0u;
     uint32_t flags = 0;
     int cnt = 0;
-    for (int u = 0; u < cnt_items; ++u) {
-        const uint32_t fl = (int32_t)pv.col[s_idx[k0 + u]] > pv.bin;
+#pragma unroll
+    for (int u = 0; u < kPartItems; ++u) {
+        const uint32_t fl = (u < cnt_items && (int32_t)bins_u[u] > pv.bin) ? 1u : 0u;
         flags |= fl << u;
         cnt += fl;
     }
@@ -1133,10 +1142,15 @@ __global__ void __launch_bounds__(kPartThreads) part_scatter_kernel(
     const int k0 = threadIdx.x * kPartItems;
     const int64_t j0 = base + k0;
     const int cnt_items = j0 >= n ? 0 : (int)(n - j0 < kPartItems ? n - j0 : kPartItems);
+    // all item loads issued before any is consumed (memory-level parallelism)
+    uint32_t bins_u[kPartItems];
+#pragma unroll
+    for (int u = 0; u < kPartItems; ++u) bins_u[u] = u < cnt_items ? (uint32_t)__ldg(pv.col + s_idx[k0 + u]) : 0u;
     uint32_t flags = 0;
     int cnt = 0;
-    for (int u = 0; u < cnt_items; ++u) {
-        const uint32_t fl = (int32_t)pv.col[s_idx[k0 + u]] > pv.bin;
+#pragma unroll
+    for (int u = 0; u < kPartItems; ++u) {
+        const uint32_t fl = (u < cnt_items && (int32_t)bins_u[u] > pv.bin) ? 1u : 0u;
         flags |= fl << u;
         cnt += fl;
     }
@@ -1202,10 +1216,19 @@ __global__ void __launch_bounds__(kPartThreads) route_final_kernel(
     const int64_t j0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * kPartItems;
     if (j0 >= n) return;
     const int cnt = (int)(n - j0 < kPartItems ? n - j0 : kPartItems);
-    walk_segments(mem_start, K, (uint32_t)j0, cnt, [&](int, uint32_t j, int k) {
-        const uint32_t i = perm ? perm[j] : j;
-        const uint32_t fl = (int32_t)pv.col[i] > pv.bin;
-        leaf[i] = (uint16_t)(mem_leaf[k] | (fl << level));
+    uint32_t rows[kPartItems], fl[kPartItems];
+#pragma unroll
+    for (int u = 0; u < kPartItems; ++u)
+        rows[u] = u < cnt ? (perm ? __ldg(perm + j0 + u) : (uint32_t)(j0 + u)) : 0u;
+#pragma unroll
+    for (int u = 0; u < kPartItems; ++u)
+        fl[u] = (u < cnt && (int32_t)__ldg(pv.col + rows[u]) > pv.bin) ? 1u : 0u;
+    walk_segments(mem_start, K, (uint32_t)j0, cnt, [&](int u, uint32_t, int k) {
+        uint32_t i = 0, f = 0;
+#pragma unroll
+        for (int v = 0; v < kPartItems; ++v)
+            if (v == u) { i = rows[v]; f = fl[v]; }
+        leaf[i] = (uint16_t)(mem_leaf[k] | (f << level));
     });
 }
 
