@@ -56,9 +56,10 @@ def _block(b: int, F: int, seed: int):
     X[nan] = np.nan
     # label ~ Bernoulli(sigmoid(sparse linear over 20 features + pairwise terms))
     gw = np.random.default_rng([seed, 1 << 30])
-    feats = gw.choice(F, size=20, replace=False)
-    coef = gw.standard_normal(20)
-    pairs = gw.choice(20, size=(10, 2))
+    k = min(20, F)
+    feats = gw.choice(F, size=k, replace=False)
+    coef = gw.standard_normal(k)
+    pairs = gw.choice(k, size=(10, 2))
     pcoef = gw.standard_normal(10) * 0.5
     Z = np.nan_to_num(X[feats].astype(np.float64))
     z = coef @ Z
