@@ -101,6 +101,12 @@ int dalloc(T** p, size_t count) {
 
 }  // namespace
 
+namespace cbgpu {
+// Sets the thread's cbgpu_last_error() message for entry points defined in
+// other translation units; returns `code`.
+int record_error(int code, const char* msg) { return fail(code, "%s", msg); }
+}  // namespace cbgpu
+
 struct cbgpu_session {
     // configuration
     int device = 0;

@@ -205,6 +205,28 @@ CBGPU_API int cbgpu_bootstrap_weights(int32_t type, int64_t n, int64_t row_offse
                             const uint64_t* rng_raw4, float sample_rate, float bagging_temperature,
                             const double* der_obj, double lambda, double* out);
 
+/* Allocation-free level histogram.  No counterpart in the reference: it exists
+ * for callers that cannot call cudaMalloc when they need a histogram (code
+ * running under CUDA graph capture, processes whose device memory belongs to
+ * their own pool allocator, hosts that forbid allocation on the hot path).
+ * Inputs and output are DEVICE pointers owned by the caller: bins row-major
+ * u8 [n][row_stride] (16-byte aligned; row_stride a multiple of 32 and at
+ * least n_features rounded up to 32), g/h f64 [n]; out f64
+ * [n_features][n_bins][2] (channel 0 = sum g, 1 = sum h), the same values
+ * cbgpu_histogram returns for one leaf.  Work is enqueued on `stream`
+ * (a cudaStream_t; NULL = the legacy default stream) and the call returns
+ * without synchronizing.  Intermediate state lives in one fixed device array
+ * of about 5.1 MiB that every GPU loading the library holds until exit; limits
+ * per call: n <= 262144 rows, n_features * n_bins <= 65536, n_bins <= 256;
+ * larger sizes return CBGPU_ERR_INVALID.  The first call on a device looks up
+ * the array's device address (once per device), so make that first call before
+ * any stream capture.  All calls share the array, which keeps the previous
+ * call's contents (each call clears what must start at zero): calls that
+ * overlap on the GPU, on different streams or from different threads, race. */
+CBGPU_API int cbgpu_histogram_noalloc(const uint8_t* d_bins_row_major, int64_t n, int32_t n_features,
+                                      int32_t row_stride, int32_t n_bins, const double* d_g,
+                                      const double* d_h, double* d_out_hist, void* stream);
+
 /* NCCL unique id (128 bytes) for world_size > 1 sessions. */
 CBGPU_API int cbgpu_nccl_unique_id(uint8_t* out128);
 
