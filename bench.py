@@ -253,13 +253,16 @@ def main():
     X, y = make_shard(row_offset, n, F, args.seed)
     borders = make_borders(F, args.border_count, args.seed)
     cols = [X[f] for f in range(F)]
-    uid = None
-    if world > 1:
+    def fresh_uid():
+        # an NCCL unique id serves one communicator: every session gets its own
+        if world == 1:
+            return None
         obj = [cb.nccl_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(obj, src=0)
-        uid = obj[0]
+        return obj[0]
 
     def open_session(sample_from_host: bool):
+        uid = fresh_uid()
         rt = cb.B200Runtime()
         cfg = cb.DeviceTrainConfig(bootstrap_type="Bayesian", bagging_temperature=1.0, rng_seed=0, bias=0.0,
                                    sample_from_host=sample_from_host, device=local_rank, rank=rank,

@@ -97,7 +97,15 @@ def fit(float_columns: Sequence[np.ndarray], borders: Sequence[Sequence[float]],
     w = None if weights is None else np.ascontiguousarray(weights, dtype=np.float64)
     pl = placement or {}
     n_total = pl.get("n_total", n)
-    sw = sum_weights if sum_weights is not None else (seq_sum(w) if w is not None else float(n))
+    # scale_l2_reg (leaf.rs:177) uses the GLOBAL weight sum and row count
+    if sum_weights is not None:
+        sw = sum_weights
+    elif w is not None:
+        if n != n_total:
+            raise ValueError("a sharded weighted fit needs sum_weights (the global weight sum)")
+        sw = seq_sum(w)
+    else:
+        sw = float(n_total)
     scaled_l2 = p.l2_leaf_reg * (sw / n_total) if n_total else p.l2_leaf_reg
     b0 = bias if bias is not None else starting_approx(p, t)
     n_bins = max(len(b) for b in borders) + 1
