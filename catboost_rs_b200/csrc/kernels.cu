@@ -9,6 +9,7 @@
 //
 // Compiled with -fmad=false: every f64 expression rounds each operation as the
 // reference's Rust code does (no FMA contraction).
+#include <algorithm>
 #include <cfloat>
 #include <cstdio>
 
@@ -589,36 +590,156 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
 
+// Tiles: as many 64-feature tiles as fit (each lane owns 2 features), then
+// one 32-feature tile if 32+ features remain, then a narrow tail of < 32
+// features whose warp step consumes 32 / width rows.  All tiles of a row
+// chunk run in one launch (blockIdx.x = tile, fastest) and share L2 lines.
+struct TileInfo {
+    int f0, nf, kind;  // kind: 2 = 64-feature tile, 1 = 32-feature tile, 0 = narrow tail
+};
+
+__host__ __device__ __forceinline__ int hist_fpl(int B) { return B <= kHistMaxBinsFpl2 ? 2 : 1; }
+
+__host__ __device__ __forceinline__ int hist_n_tiles(int F, int fpl) {
+    const int w = 32 * fpl;
+    const int nfull = F / w, rem = F % w;
+    return nfull + (fpl == 2 && rem >= 32 ? 1 : 0) + ((fpl == 2 ? rem % 32 : rem) > 0 ? 1 : 0);
+}
+
+__device__ __forceinline__ TileInfo hist_tile(int F, int fpl, int t) {
+    const int w = 32 * fpl;
+    const int nfull = F / w, rem = F % w;
+    if (t < nfull) return TileInfo{t * w, w, fpl};
+    int f0 = nfull * w;
+    if (fpl == 2 && rem >= 32) {
+        if (t == nfull) return TileInfo{f0, 32, 1};
+        f0 += 32;
+    }
+    return TileInfo{f0, F - f0, 0};
+}
+
+// One staged group of up to 32 rows for a tile whose lanes each own kFpl
+// features and whose warp step covers kRows = 32 / kWt rows.
+template <int kFpl, int kWt>
+__device__ __forceinline__ void hist_group(uint32_t* __restrict__ hs, const uint8_t* __restrict__ sb,
+                                           const uint4* __restrict__ ss, uint32_t cnt, int lane, int nf) {
+    constexpr int kRows = 32 / kWt;
+    constexpr int kCols = 32 * kFpl;  // u32 columns per (bin, part) row of the table
+    const int sub = lane / kWt, fl = lane % kWt;
+    if (fl * kFpl >= nf) return;
+    const bool second = kFpl == 2 && fl * 2 + 1 < nf;
+    uint32_t* my = hs + lane;
+    uint32_t u = sub;
+    for (; u + 3 * kRows < cnt; u += 4 * kRows) {
+        uint32_t b[4][kFpl];
+        uint4 s[4];
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+            const uint32_t r = u + v * kRows;
+            if (kFpl == 2) {
+                const uint32_t two = *(const uint16_t*)(sb + r * 64 + fl * 2);
+                b[v][0] = two & 0xffu;
+                b[v][kFpl - 1] = two >> 8;
+            } else {
+                b[v][0] = sb[r * 32 + fl];
+            }
+            s[v] = ss[r];
+        }
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+#pragma unroll
+            for (int j = 0; j < kFpl; ++j) {
+                if (j == 1 && !second) continue;
+                uint32_t* cc = my + b[v][j] * (4 * kCols) + j * 32;
+                atomicAdd(cc, s[v].x);
+                atomicAdd(cc + kCols, s[v].y);
+                atomicAdd(cc + 2 * kCols, s[v].z);
+                atomicAdd(cc + 3 * kCols, s[v].w);
+            }
+        }
+    }
+    for (; u < cnt; u += kRows) {
+        uint32_t b0, b1 = 0;
+        if (kFpl == 2) {
+            const uint32_t two = *(const uint16_t*)(sb + u * 64 + fl * 2);
+            b0 = two & 0xffu;
+            b1 = two >> 8;
+        } else {
+            b0 = sb[u * 32 + fl];
+        }
+        const uint4 s = ss[u];
+#pragma unroll
+        for (int j = 0; j < kFpl; ++j) {
+            if (j == 1 && !second) continue;
+            uint32_t* cc = my + (j ? b1 : b0) * (4 * kCols) + j * 32;
+            atomicAdd(cc, s.x);
+            atomicAdd(cc + kCols, s.y);
+            atomicAdd(cc + 2 * kCols, s.z);
+            atomicAdd(cc + 3 * kCols, s.w);
+        }
+    }
+}
+
+// Flush: column j*32 + lane of a kFpl tile holds feature lane*kFpl + j; for a
+// narrow tile (kFpl 1, width kWt) the columns r*kWt + f (r < 32/kWt) all hold
+// feature f and are summed.  Each column's (lo, hi) parts recombine exactly.
+template <int kFpl, int kWt>
+__device__ __forceinline__ void hist_flush(const uint32_t* __restrict__ hs, int B, int nf,
+                                           ull* __restrict__ out) {
+    constexpr int kRows = 32 / kWt;
+    constexpr int kCols = 32 * kFpl;
+    for (int k = threadIdx.x; k < B * 32 * kFpl; k += blockDim.x) {
+        const int b = k / (32 * kFpl), c = k % (32 * kFpl);
+        int f;  // feature within the tile
+        if (kFpl == 2) f = (c & 31) * 2 + (c >> 5);
+        else f = c;
+        if (kWt < 32 && c >= kWt) continue;
+        if (f >= nf) continue;
+        long long gsum = 0, hsum = 0;
+#pragma unroll
+        for (int r = 0; r < kRows; ++r) {
+            const uint32_t* cc = hs + b * 4 * kCols + r * kWt + c;
+            gsum += (long long)(int32_t)cc[kCols] * (1ll << kPackSplit) + (long long)cc[0];
+            hsum += (long long)(int32_t)cc[3 * kCols] * (1ll << kPackSplit) + (long long)cc[2 * kCols];
+        }
+        ull* o = out + ((size_t)f * B + b) * 2;
+        if (gsum) atomicAdd(o, (ull)gsum);
+        if (hsum) atomicAdd(o + 1, (ull)hsum);
+    }
+}
+
 // Each warp streams its rows in groups of 32 through a kHistStages-deep ring
-// of shared-memory stages: lane l copies row l's 32-byte tile slice (2 x 16 B)
+// of shared-memory stages: lane l copies row l's tile slice (16-byte pieces)
 // and its 16-byte packed stats with cp.async, so one warp instruction moves
-// 512 B and many groups are in flight.  A staged group is then consumed with
-// lane = feature: one byte load of (row, lane), one broadcast load of the row's
-// stats and four conflict-free 32-bit shared reductions.
-template <bool kGather>
-__global__ void __launch_bounds__(kHistThreads, 2) hist_kernel(
+// 512 B and several groups are in flight.  A staged group is then consumed
+// with lane = (row slot, features): one byte (or u16) load per lane, one load
+// of the row's stats, and four conflict-free 32-bit shared reductions per
+// feature into the lane's own column (bank = lane).  Reductions and shared
+// loads issue through the MIO queue, which bounds this kernel: owning two
+// features per lane spends the two loads on eight reductions instead of four.
+template <bool kGather, int kFplFull>
+__global__ void __launch_bounds__(kHistThreads, 1) hist_kernel(
     const uint8_t* __restrict__ bins_rm, int32_t F_pad, int32_t F, int32_t B,
     const uint4* __restrict__ qstats, const uint32_t* __restrict__ perm,
     const HistChunk* __restrict__ chunks, const uint32_t* __restrict__ n_chunks,
     ull* __restrict__ built) {
-    extern __shared__ __align__(16) uint32_t hs[];  // [B][4][32] then the staging ring
-    // blockIdx.x = feature tile (fastest), so the tiles of one row chunk run
-    // together and share the L2 lines of those rows; blocks stride over chunks
-    // when there are more than gridDim.y.
-    const int tile = blockIdx.x;
+    extern __shared__ __align__(16) uint32_t hs[];  // table [B][4][32*fpl] then the staging ring
+    const TileInfo ti = hist_tile(F, kFplFull, blockIdx.x);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     constexpr int kWarps = kHistThreads / 32;
-    uint8_t* sbins = (uint8_t*)(hs + B * 128) + (size_t)warp * kHistStages * 32 * 32;
-    uint4* sstat = (uint4*)((uint8_t*)(hs + B * 128) + (size_t)kWarps * kHistStages * 32 * 32) +
+    constexpr int kSlice = 32 * kFplFull;  // staged bytes per row
+    const size_t table_words = (size_t)B * 128 * kFplFull;
+    uint8_t* sbins = (uint8_t*)(hs + table_words) + (size_t)warp * kHistStages * 32 * kSlice;
+    uint4* sstat = (uint4*)((uint8_t*)(hs + table_words) + (size_t)kWarps * kHistStages * 32 * kSlice) +
                    (size_t)warp * kHistStages * 32;
-    const int f = tile * kTile + lane;
-    const bool active = f < F;
-    uint32_t* my = hs + lane;
-    const uint8_t* tile_base = bins_rm + tile * kTile;
+    // 16-byte pieces of the row slice this tile needs
+    const int pieces = ti.kind == 2 ? 4 : (ti.kind == 1 ? 2 : (ti.nf > 16 ? 2 : 1));
+    const int narrow_w = ti.nf > 16 ? 32 : ti.nf > 8 ? 16 : ti.nf > 4 ? 8 : ti.nf > 2 ? 4 : ti.nf > 1 ? 2 : 1;
+    const uint8_t* tile_base = bins_rm + ti.f0;
     const uint32_t nch = *n_chunks;
     for (uint32_t c = blockIdx.y; c < nch; c += gridDim.y) {
     const HistChunk ck = chunks[c];
-    for (int k = threadIdx.x; k < B * 128; k += blockDim.x) hs[k] = 0u;
+    for (size_t k = threadIdx.x; k < table_words; k += blockDim.x) hs[k] = 0u;
     __syncthreads();
 
     const uint32_t start = ck.start, len = ck.len;
@@ -632,10 +753,9 @@ __global__ void __launch_bounds__(kHistThreads, 2) hist_kernel(
     };
     auto issue = [&](uint32_t i, int st) {
         if (i != 0xffffffffu) {
-            uint8_t* d = sbins + ((size_t)st * 32 + lane) * 32;
+            uint8_t* d = sbins + ((size_t)st * 32 + lane) * kSlice;
             const uint8_t* src = tile_base + (size_t)i * F_pad;
-            cp_async16(d, src);
-            cp_async16(d + 16, src + 16);
+            for (int p = 0; p < pieces; ++p) cp_async16(d + 16 * p, src + 16 * p);
             cp_async16(sstat + st * 32 + lane, qstats + i);
         }
         cp_async_commit();
@@ -655,80 +775,85 @@ __global__ void __launch_bounds__(kHistThreads, 2) hist_kernel(
         cp_async_wait<kHistStages - 1>();
         __syncwarp();
         const uint32_t cnt = len - (g << 5) < 32u ? len - (g << 5) : 32u;
-        const uint8_t* sb = sbins + (size_t)st * 32 * 32 + lane;
+        const uint8_t* sb = sbins + (size_t)st * 32 * kSlice;
         const uint4* ss = sstat + st * 32;
-        if (active) {
-            uint32_t u = 0;
-            for (; u + 4 <= cnt; u += 4) {
-                uint32_t b[4];
-                uint4 s[4];
-#pragma unroll
-                for (int v = 0; v < 4; ++v) {
-                    b[v] = sb[(u + v) * 32];
-                    s[v] = ss[u + v];
-                }
-#pragma unroll
-                for (int v = 0; v < 4; ++v) {
-                    uint32_t* cc = my + b[v] * 128;
-                    atomicAdd(cc, s[v].x);
-                    atomicAdd(cc + 32, s[v].y);
-                    atomicAdd(cc + 64, s[v].z);
-                    atomicAdd(cc + 96, s[v].w);
-                }
+        // staged rows are kSlice bytes apart; the narrow / 32-wide bodies index
+        // rows 32 bytes apart, so they read the ring through a 32-byte view
+        if (kFplFull == 2 && ti.kind == 2) {
+            hist_group<2, 32>(hs, sb, ss, cnt, lane, ti.nf);
+        } else {
+            // kFplFull == 2 stages 64-byte rows: re-point the row stride
+            const uint8_t* sb32 = sb;
+            uint32_t* tab = hs;
+            if (kFplFull == 2) {
+                // compact this group's 32-byte slices in place (rows 64 B apart -> 32 B apart)
+                __syncwarp();
+                uint8_t* w = (uint8_t*)sb;
+                const uint4 lo = *(const uint4*)(sb + lane * 64), hi = *(const uint4*)(sb + lane * 64 + 16);
+                __syncwarp();
+                *(uint4*)(w + lane * 32) = lo;
+                *(uint4*)(w + lane * 32 + 16) = hi;
+                __syncwarp();
             }
-            for (; u < cnt; ++u) {
-                const uint32_t bb = sb[u * 32];
-                const uint4 s = ss[u];
-                uint32_t* cc = my + bb * 128;
-                atomicAdd(cc, s.x);
-                atomicAdd(cc + 32, s.y);
-                atomicAdd(cc + 64, s.z);
-                atomicAdd(cc + 96, s.w);
-            }
+            if (ti.kind == 1 || narrow_w == 32) hist_group<1, 32>(tab, sb32, ss, cnt, lane, ti.nf);
+            else if (narrow_w == 16) hist_group<1, 16>(tab, sb32, ss, cnt, lane, ti.nf);
+            else if (narrow_w == 8) hist_group<1, 8>(tab, sb32, ss, cnt, lane, ti.nf);
+            else if (narrow_w == 4) hist_group<1, 4>(tab, sb32, ss, cnt, lane, ti.nf);
+            else if (narrow_w == 2) hist_group<1, 2>(tab, sb32, ss, cnt, lane, ti.nf);
+            else hist_group<1, 1>(tab, sb32, ss, cnt, lane, ti.nf);
         }
         __syncwarp();  // the stage is refilled next iteration
         st = (st + 1) % kHistStages;
     }
     cp_async_wait<0>();
     __syncthreads();
-    const int nf = F - tile * kTile < kTile ? F - tile * kTile : kTile;
-    ull* out = built + ((size_t)ck.slot * F + (size_t)tile * kTile) * B * 2;
-    for (int k = threadIdx.x; k < B * 32; k += blockDim.x) {
-        const int b = k >> 5, l = k & 31;
-        if (l >= nf) continue;
-        const uint32_t* cc = hs + b * 128 + l;
-        const long long gsum = (long long)(int32_t)cc[32] * (1ll << kPackSplit) + (long long)cc[0];
-        const long long hsum = (long long)(int32_t)cc[96] * (1ll << kPackSplit) + (long long)cc[64];
-        ull* o = out + ((size_t)l * B + b) * 2;
-        if (gsum) atomicAdd(o, (ull)gsum);
-        if (hsum) atomicAdd(o + 1, (ull)hsum);
-    }
-    __syncthreads();  // the histogram is zeroed again for the next chunk
+    ull* out = built + ((size_t)ck.slot * F + (size_t)ti.f0) * B * 2;
+    if (kFplFull == 2 && ti.kind == 2) hist_flush<2, 32>(hs, B, ti.nf, out);
+    else if (ti.kind == 1 || narrow_w == 32) hist_flush<1, 32>(hs, B, ti.nf, out);
+    else if (narrow_w == 16) hist_flush<1, 16>(hs, B, ti.nf, out);
+    else if (narrow_w == 8) hist_flush<1, 8>(hs, B, ti.nf, out);
+    else if (narrow_w == 4) hist_flush<1, 4>(hs, B, ti.nf, out);
+    else if (narrow_w == 2) hist_flush<1, 2>(hs, B, ti.nf, out);
+    else hist_flush<1, 1>(hs, B, ti.nf, out);
+    __syncthreads();  // the table is zeroed again for the next chunk
     }
 }
 
 size_t hist_smem_bytes(int32_t B) {
-    return sizeof(uint32_t) * (size_t)B * 128 + (size_t)(kHistThreads / 32) * kHistStages * 32 * (32 + 16);
+    const int fpl = hist_fpl(B);
+    return sizeof(uint32_t) * (size_t)B * 128 * fpl +
+           (size_t)(kHistThreads / 32) * kHistStages * 32 * (32 * fpl + 16);
+}
+
+template <bool kGather, int kFpl>
+static void launch_hist_variant(unsigned gy, cudaStream_t st, const uint8_t* bins_rm, int32_t F_pad, int32_t F,
+                                int32_t B, const uint4* qstats, const uint32_t* perm, const HistChunk* chunks,
+                                const uint32_t* n_chunks, ull* built) {
+    static int attr_device = -1;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (attr_device != dev) {
+        cudaFuncSetAttribute(hist_kernel<kGather, kFpl>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        attr_device = dev;
+    }
+    const dim3 grid((unsigned)hist_n_tiles(F, kFpl), gy);
+    hist_kernel<kGather, kFpl><<<grid, kHistThreads, hist_smem_bytes(B), st>>>(bins_rm, F_pad, F, B, qstats,
+                                                                              perm, chunks, n_chunks, built);
 }
 
 void launch_hist(const uint8_t* bins_rm, int32_t F_pad, int32_t F, int32_t B, const uint4* qstats,
                  const uint32_t* perm, const HistChunk* chunks, const uint32_t* n_chunks,
                  uint32_t max_chunks, ull* built, cudaStream_t st) {
     if (max_chunks == 0) return;
-    const size_t smem = hist_smem_bytes(B);
-    static bool attr = false;
-    if (!attr) {
-        cudaFuncSetAttribute(hist_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        cudaFuncSetAttribute(hist_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        attr = true;
+    const unsigned gy = max_chunks < 65535u ? max_chunks : 65535u;
+    const bool two = hist_fpl(B) == 2;
+    if (perm) {
+        if (two) launch_hist_variant<true, 2>(gy, st, bins_rm, F_pad, F, B, qstats, perm, chunks, n_chunks, built);
+        else launch_hist_variant<true, 1>(gy, st, bins_rm, F_pad, F, B, qstats, perm, chunks, n_chunks, built);
+    } else {
+        if (two) launch_hist_variant<false, 2>(gy, st, bins_rm, F_pad, F, B, qstats, perm, chunks, n_chunks, built);
+        else launch_hist_variant<false, 1>(gy, st, bins_rm, F_pad, F, B, qstats, perm, chunks, n_chunks, built);
     }
-    dim3 grid((unsigned)((F + kTile - 1) / kTile), max_chunks < 65535u ? max_chunks : 65535u);
-    if (perm)
-        hist_kernel<true><<<grid, kHistThreads, smem, st>>>(bins_rm, F_pad, F, B, qstats, perm, chunks,
-                                                             n_chunks, built);
-    else
-        hist_kernel<false><<<grid, kHistThreads, smem, st>>>(bins_rm, F_pad, F, B, qstats, perm, chunks,
-                                                              n_chunks, built);
 }
 
 // Work list for the level: level 0 = all rows (identity order) in one slot;
@@ -1014,16 +1139,47 @@ __device__ __forceinline__ void walk_segments(const uint32_t* __restrict__ mem_s
     }
 }
 
+// The chosen split's outcome for every row, as a bit array in natural row
+// order (bit i of word i/32 = bin > border): one coalesced pass over the
+// feature's column, so the partition kernels gather bits from a 1.25 MB array
+// (10M rows) instead of bytes from the 10 MB column.
+__global__ void __launch_bounds__(256) split_flags_kernel(int level, int64_t n,
+                                                          const uint8_t* __restrict__ bins_fm,
+                                                          int64_t n_stride,
+                                                          const TreeState* __restrict__ ts,
+                                                          uint32_t* __restrict__ flags) {
+    const PartView pv = part_view(ts, level, bins_fm, n_stride);
+    const int64_t words = (n + 31) >> 5;
+    for (int64_t w = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; w < words;
+         w += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r0 = w << 5;
+        uint32_t bits = 0;
+        if (r0 + 32 <= n) {
+            const uint4* p = (const uint4*)(pv.col + r0);  // n_stride and r0 are multiples of 16
+            const uint4 a = __ldg(p), b = __ldg(p + 1);
+            const uint32_t v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+            for (int k = 0; k < 32; ++k)
+                bits |= (uint32_t)((int32_t)((v[k >> 2] >> ((k & 3) * 8)) & 0xffu) > pv.bin) << k;
+        } else {
+            for (int k = 0; r0 + k < n; ++k) bits |= (uint32_t)((int32_t)pv.col[r0 + k] > pv.bin) << k;
+        }
+        flags[w] = bits;
+    }
+}
+
+__device__ __forceinline__ uint32_t flag_of(const uint32_t* __restrict__ flags, uint32_t i) {
+    return (__ldg(flags + (i >> 5)) >> (i & 31)) & 1u;
+}
+
 __global__ void __launch_bounds__(kPartThreads) part_count_kernel(
-    int level, int64_t n, const uint8_t* __restrict__ bins_fm, int64_t n_stride,
-    const uint32_t* __restrict__ perm, const uint32_t* __restrict__ seg_cnt,
+    int level, int64_t n, const uint32_t* __restrict__ flags_nat, const uint32_t* __restrict__ perm, const uint32_t* __restrict__ seg_cnt,
     const uint32_t* __restrict__ mem_start, const uint32_t* __restrict__ mem_leaf,
     uint32_t* __restrict__ seg_start_blk, uint32_t* __restrict__ seg_start_part,
     uint32_t* __restrict__ seg_end_blk, uint32_t* __restrict__ seg_end_part,
-    uint32_t* __restrict__ blk_true, const TreeState* __restrict__ ts) {
+    uint32_t* __restrict__ blk_true) {
     __shared__ uint32_t s_idx[kPartTile];
     __shared__ uint32_t s_scan[40];
-    const PartView pv = part_view(ts, level, bins_fm, n_stride);
     const int K = 1 << level;
     const int64_t base = (int64_t)blockIdx.x * kPartTile;
     for (int k = threadIdx.x; k < kPartTile; k += blockDim.x) {
@@ -1035,16 +1191,15 @@ __global__ void __launch_bounds__(kPartThreads) part_count_kernel(
     const int64_t j0 = base + k0;
     const int cnt_items = j0 >= n ? 0 : (int)(n - j0 < kPartItems ? n - j0 : kPartItems);
     // all item loads issued before any is consumed (memory-level parallelism)
-    uint32_t bins_u[kPartItems];
+    uint32_t fl_u[kPartItems];
 #pragma unroll
-    for (int u = 0; u < kPartItems; ++u) bins_u[u] = u < cnt_items ? (uint32_t)__ldg(pv.col + s_idx[k0 + u]) : 0u;
+    for (int u = 0; u < kPartItems; ++u) fl_u[u] = u < cnt_items ? flag_of(flags_nat, s_idx[k0 + u]) : 0u;
     uint32_t flags = 0;
     int cnt = 0;
 #pragma unroll
     for (int u = 0; u < kPartItems; ++u) {
-        const uint32_t fl = (u < cnt_items && (int32_t)bins_u[u] > pv.bin) ? 1u : 0u;
-        flags |= fl << u;
-        cnt += fl;
+        flags |= fl_u[u] << u;
+        cnt += fl_u[u];
     }
     uint32_t tot;
     const uint32_t excl = block_excl_scan<uint32_t>((uint32_t)cnt, s_scan, &tot);
@@ -1123,15 +1278,13 @@ __global__ void __launch_bounds__(1024) part_scan_kernel(
 }
 
 __global__ void __launch_bounds__(kPartThreads) part_scatter_kernel(
-    int level, int64_t n, const uint8_t* __restrict__ bins_fm, int64_t n_stride,
+    int level, int64_t n, const uint32_t* __restrict__ flags_nat,
     const uint32_t* __restrict__ perm, uint32_t* __restrict__ perm_next,
     const uint32_t* __restrict__ seg_off, const uint32_t* __restrict__ mem_start,
     const uint32_t* __restrict__ mem_leaf, const uint32_t* __restrict__ blk_off,
-    const uint32_t* __restrict__ t_start, const uint32_t* __restrict__ f_cnt,
-    const TreeState* __restrict__ ts) {
+    const uint32_t* __restrict__ t_start, const uint32_t* __restrict__ f_cnt) {
     __shared__ uint32_t s_idx[kPartTile];
     __shared__ uint32_t s_scan[40];
-    const PartView pv = part_view(ts, level, bins_fm, n_stride);
     const int K = 1 << level;
     const int64_t base = (int64_t)blockIdx.x * kPartTile;
     for (int k = threadIdx.x; k < kPartTile; k += blockDim.x) {
@@ -1143,16 +1296,15 @@ __global__ void __launch_bounds__(kPartThreads) part_scatter_kernel(
     const int64_t j0 = base + k0;
     const int cnt_items = j0 >= n ? 0 : (int)(n - j0 < kPartItems ? n - j0 : kPartItems);
     // all item loads issued before any is consumed (memory-level parallelism)
-    uint32_t bins_u[kPartItems];
+    uint32_t fl_u[kPartItems];
 #pragma unroll
-    for (int u = 0; u < kPartItems; ++u) bins_u[u] = u < cnt_items ? (uint32_t)__ldg(pv.col + s_idx[k0 + u]) : 0u;
+    for (int u = 0; u < kPartItems; ++u) fl_u[u] = u < cnt_items ? flag_of(flags_nat, s_idx[k0 + u]) : 0u;
     uint32_t flags = 0;
     int cnt = 0;
 #pragma unroll
     for (int u = 0; u < kPartItems; ++u) {
-        const uint32_t fl = (u < cnt_items && (int32_t)bins_u[u] > pv.bin) ? 1u : 0u;
-        flags |= fl << u;
-        cnt += fl;
+        flags |= fl_u[u] << u;
+        cnt += fl_u[u];
     }
     const uint32_t excl = block_excl_scan<uint32_t>((uint32_t)cnt, s_scan, nullptr);
     if (cnt_items == 0) return;
@@ -1169,19 +1321,22 @@ __global__ void __launch_bounds__(kPartThreads) part_scatter_kernel(
 
 void launch_partition(int level, int64_t n, const uint8_t* bins_fm, int64_t n_stride,
                       const uint32_t* perm, uint32_t* perm_next, SegTables& sg, uint32_t* blk_true,
-                      uint32_t* child_cnt, TreeState* ts, cudaStream_t st) {
+                      uint32_t* flags, uint32_t* child_cnt, TreeState* ts, cudaStream_t st) {
     const uint32_t tiles = (uint32_t)((n + kPartTile - 1) / kPartTile);
     if (tiles == 0) return;
-    part_count_kernel<<<tiles, kPartThreads, 0, st>>>(level, n, bins_fm, n_stride, perm, sg.seg_cnt,
-                                                       sg.mem_start, sg.mem_leaf, sg.start_blk,
-                                                       sg.start_part, sg.end_blk, sg.end_part, blk_true, ts);
+    const int64_t words = (n + 31) >> 5;
+    split_flags_kernel<<<(unsigned)std::min<int64_t>((words + 255) / 256, 148 * 8), 256, 0, st>>>(
+        level, n, bins_fm, n_stride, ts, flags);
+    part_count_kernel<<<tiles, kPartThreads, 0, st>>>(level, n, flags, perm, sg.seg_cnt, sg.mem_start,
+                                                       sg.mem_leaf, sg.start_blk, sg.start_part, sg.end_blk,
+                                                       sg.end_part, blk_true);
     part_scan_kernel<<<1, 1024, 0, st>>>(level, tiles, blk_true, sg.seg_off, sg.seg_cnt, sg.mem_leaf,
                                          sg.start_blk, sg.start_part, sg.end_blk, sg.end_part, sg.t_start,
                                          sg.f_cnt, child_cnt, sg.seg_off_next, sg.seg_cnt_next,
                                          sg.mem_start_next, sg.mem_leaf_next);
-    part_scatter_kernel<<<tiles, kPartThreads, 0, st>>>(level, n, bins_fm, n_stride, perm, perm_next,
-                                                         sg.seg_off, sg.mem_start, sg.mem_leaf, blk_true,
-                                                         sg.t_start, sg.f_cnt, ts);
+    part_scatter_kernel<<<tiles, kPartThreads, 0, st>>>(level, n, flags, perm, perm_next, sg.seg_off,
+                                                         sg.mem_start, sg.mem_leaf, blk_true, sg.t_start,
+                                                         sg.f_cnt);
     sg.swap();
 }
 
@@ -1207,11 +1362,9 @@ void launch_small_side(int level_next, const uint32_t* child_cnt_global, uint8_t
 // channels) as exact int64 sums.
 // ============================================================================
 __global__ void __launch_bounds__(kPartThreads) route_final_kernel(
-    int level, int64_t n, const uint8_t* __restrict__ bins_fm, int64_t n_stride,
+    int level, int64_t n, const uint32_t* __restrict__ flags_nat,
     const uint32_t* __restrict__ perm, const uint32_t* __restrict__ mem_start,
-    const uint32_t* __restrict__ mem_leaf, uint16_t* __restrict__ leaf,
-    const TreeState* __restrict__ ts) {
-    const PartView pv = part_view(ts, level, bins_fm, n_stride);
+    const uint32_t* __restrict__ mem_leaf, uint16_t* __restrict__ leaf) {
     const int K = 1 << level;
     const int64_t j0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * kPartItems;
     if (j0 >= n) return;
@@ -1222,7 +1375,7 @@ __global__ void __launch_bounds__(kPartThreads) route_final_kernel(
         rows[u] = u < cnt ? (perm ? __ldg(perm + j0 + u) : (uint32_t)(j0 + u)) : 0u;
 #pragma unroll
     for (int u = 0; u < kPartItems; ++u)
-        fl[u] = (u < cnt && (int32_t)__ldg(pv.col + rows[u]) > pv.bin) ? 1u : 0u;
+        fl[u] = u < cnt ? flag_of(flags_nat, rows[u]) : 0u;
     walk_segments(mem_start, K, (uint32_t)j0, cnt, [&](int u, uint32_t, int k) {
         uint32_t i = 0, f = 0;
 #pragma unroll
@@ -1261,13 +1414,16 @@ __global__ void __launch_bounds__(256) leafsum_kernel(int64_t n, const uint16_t*
 }
 
 void launch_route_leafsum(int level, int64_t n, const uint8_t* bins_fm, int64_t n_stride,
-                          const uint32_t* perm, const SegTables& sg, uint16_t* leaf, const double* wd1,
-                          const double* weight, int depth, TreeState* ts, ull* leaf_sums,
+                          const uint32_t* perm, const SegTables& sg, uint32_t* flags, uint16_t* leaf,
+                          const double* wd1, const double* weight, int depth, TreeState* ts, ull* leaf_sums,
                           cudaStream_t st) {
     if (n <= 0) return;
+    const int64_t words = (n + 31) >> 5;
+    split_flags_kernel<<<(unsigned)std::min<int64_t>((words + 255) / 256, 148 * 8), 256, 0, st>>>(
+        level, n, bins_fm, n_stride, ts, flags);
     const int64_t threads = (n + kPartItems - 1) / kPartItems;
     route_final_kernel<<<(unsigned)((threads + kPartThreads - 1) / kPartThreads), kPartThreads, 0, st>>>(
-        level, n, bins_fm, n_stride, perm, sg.mem_start, sg.mem_leaf, leaf, ts);
+        level, n, flags, perm, sg.mem_start, sg.mem_leaf, leaf);
     int64_t blocks = (n + 255) / 256;
     if (blocks > 148 * 4) blocks = 148 * 4;
     const size_t smem = depth <= 10 ? sizeof(ull) * 2 * (1 << depth) : 0;

@@ -48,6 +48,7 @@ struct TreeState {
 constexpr int kTile = 32;          // features per histogram tile (one per lane)
 constexpr int kHistThreads = 256;  // 8 warps
 constexpr int kHistStages = 3;     // cp.async ring depth per warp (groups of 32 rows)
+constexpr int kHistMaxBinsFpl2 = 160;  // up to this many bins a lane owns 2 features (shared-memory budget)
 constexpr int kChunkRows = 16384;  // rows per histogram work item
 // Score-channel fixed point: |row value| <= 2^kPackBits, split at bit kPackSplit
 // into (lo, hi) u32 parts whose sums over kChunkRows rows stay below 2^31.
@@ -118,15 +119,15 @@ void launch_derive_prefix(int level, int32_t F, int32_t B, const ull* built, con
 void launch_score(int level, int32_t F, int32_t B, const ull* cur, const int32_t* border_counts,
                   double l2, int score_fn, double* feat_score, int32_t* feat_bin, TreeState* ts,
                   cudaStream_t st);
-// blk_true: ceil(n / kPartTile) + 1; child_cnt: 2^(level+1) (false counts, then true).
+// flags: ceil(n / 32) words (the split outcome bits); blk_true: ceil(n / kPartTile) + 1; child_cnt: 2^(level+1) (false counts, then true).
 void launch_partition(int level, int64_t n, const uint8_t* bins_fm, int64_t n_stride,
                       const uint32_t* perm, uint32_t* perm_next, SegTables& sg, uint32_t* blk_true,
-                      uint32_t* child_cnt, TreeState* ts, cudaStream_t st);
+                      uint32_t* flags, uint32_t* child_cnt, TreeState* ts, cudaStream_t st);
 void launch_small_side(int level_next, const uint32_t* child_cnt_global, uint8_t* small_side,
                        cudaStream_t st);
 void launch_route_leafsum(int level, int64_t n, const uint8_t* bins_fm, int64_t n_stride,
-                          const uint32_t* perm, const SegTables& sg, uint16_t* leaf, const double* wd1,
-                          const double* weight, int depth, TreeState* ts, ull* leaf_sums,
+                          const uint32_t* perm, const SegTables& sg, uint32_t* flags, uint16_t* leaf,
+                          const double* wd1, const double* weight, int depth, TreeState* ts, ull* leaf_sums,
                           cudaStream_t st);
 void launch_leaf_values(int depth, int n_splits_expected, const ull* leaf_sums, double l2, double lr,
                         TreeState* ts, double* leaf_raw, double* leaf_lrv, cudaStream_t st);

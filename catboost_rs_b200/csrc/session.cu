@@ -143,6 +143,7 @@ struct cbgpu_session {
     SegTables sg{};
     uint32_t* blk_true = nullptr;
     uint32_t* child_cnt = nullptr;
+    uint32_t* flags = nullptr;    // split outcome bit per row (natural order)
     uint8_t* small_side = nullptr;
     HistChunk* chunks = nullptr;
     uint32_t* n_chunks = nullptr;
@@ -262,6 +263,7 @@ int alloc_session(cbgpu_session* s, const cbgpu_begin_args* a) {
     }
     DA(s->blk_true, (n + kPartTile - 1) / kPartTile + 1);
     DA(s->child_cnt, 1 << 17);
+    DA(s->flags, (n + 31) / 32 + 1);
     DA(s->small_side, 1 << 16);
     const size_t max_chunks = (size_t)(n / kChunkRows) + (L / 2) + 2;
     DA(s->chunks, max_chunks);
@@ -308,7 +310,7 @@ void free_session(cbgpu_session* s) {
     if (s->st) cudaStreamSynchronize(s->st);
     void* ptrs[] = {s->bins_rm, s->bins_fm, s->d_border_counts, s->target, s->weight, s->approx,
                     s->wd1, s->qstats, s->sw32, s->sw64, s->mvs_thr, s->leaf, s->perm[0], s->perm[1],
-                    s->seg_mem, s->blk_true, s->child_cnt, s->small_side, s->chunks, s->n_chunks, s->built,
+                    s->seg_mem, s->blk_true, s->child_cnt, s->flags, s->small_side, s->chunks, s->n_chunks, s->built,
                     s->hist[0], s->hist[1], s->feat_score, s->feat_bin, s->leaf_sums, s->leaf_raw,
                     s->leaf_lrv, s->ts, s->d_err, s->leaf_export};
     for (void* p : ptrs)
@@ -534,18 +536,18 @@ int grow(cbgpu_session* s, const double* approx_h, const double* target_h, int64
         rec(e + 3);
         if (l + 1 < D) {
             launch_partition(l, s->n, s->bins_fm, s->n_stride, l == 0 ? nullptr : s->perm[pp],
-                             s->perm[pp ^ 1], s->sg, s->blk_true, s->child_cnt, s->ts, st);
+                             s->perm[pp ^ 1], s->sg, s->blk_true, s->flags, s->child_cnt, s->ts, st);
             pp ^= 1;
             rec(e + 4);
             int rc = allreduce(s, s->child_cnt, (size_t)2 << l, ncclUint32, ncclSum);
             if (rc) return rc;
             launch_small_side(l + 1, s->child_cnt, s->small_side, st);
-            launches += 4;
+            launches += 5;
         } else {
             CU(cudaMemsetAsync(s->leaf_sums, 0, sizeof(ull) * 2 * L, st));
             launch_route_leafsum(l, s->n, s->bins_fm, s->n_stride, l == 0 ? nullptr : s->perm[pp], s->sg,
-                                 s->leaf, s->wd1, s->weight, D, s->ts, s->leaf_sums, st);
-            launches += 2;
+                                 s->flags, s->leaf, s->wd1, s->weight, D, s->ts, s->leaf_sums, st);
+            launches += 3;
             rec(e + 4);
             int rc = allreduce(s, s->leaf_sums, (size_t)2 * L, ncclUint64, ncclSum);
             if (rc) return rc;
