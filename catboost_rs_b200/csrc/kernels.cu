@@ -598,8 +598,6 @@ struct TileInfo {
     int f0, nf, kind;  // kind: 2 = 64-feature tile, 1 = 32-feature tile, 0 = narrow tail
 };
 
-__host__ __device__ __forceinline__ int hist_fpl(int B) { return B <= kHistMaxBinsFpl2 ? 2 : 1; }
-
 __host__ __device__ __forceinline__ int hist_n_tiles(int F, int fpl) {
     const int w = 32 * fpl;
     const int nfull = F / w, rem = F % w;
@@ -620,14 +618,14 @@ __device__ __forceinline__ TileInfo hist_tile(int F, int fpl, int t) {
 
 // One staged group of up to 32 rows for a tile whose lanes each own kFpl
 // features and whose warp step covers kRows = 32 / kWt rows.
-template <int kFpl, int kWt>
+template <int kFpl, int kWt, bool kFull = false>
 __device__ __forceinline__ void hist_group(uint32_t* __restrict__ hs, const uint8_t* __restrict__ sb,
                                            const uint4* __restrict__ ss, uint32_t cnt, int lane, int nf) {
     constexpr int kRows = 32 / kWt;
     constexpr int kCols = 32 * kFpl;  // u32 columns per (bin, part) row of the table
     const int sub = lane / kWt, fl = lane % kWt;
-    if (fl * kFpl >= nf) return;
-    const bool second = kFpl == 2 && fl * 2 + 1 < nf;
+    if (!kFull && fl * kFpl >= nf) return;
+    const bool second = kFull || (kFpl == 2 && fl * 2 + 1 < nf);
     uint32_t* my = hs + lane;
     uint32_t u = sub;
     for (; u + 3 * kRows < cnt; u += 4 * kRows) {
@@ -708,7 +706,7 @@ __device__ __forceinline__ void hist_flush(const uint32_t* __restrict__ hs, int 
     }
 }
 
-// Each warp streams its rows in groups of 32 through a kHistStages-deep ring
+// Each warp streams its rows in groups of 32 through a kStages-deep ring
 // of shared-memory stages: lane l copies row l's tile slice (16-byte pieces)
 // and its 16-byte packed stats with cp.async, so one warp instruction moves
 // 512 B and several groups are in flight.  A staged group is then consumed
@@ -717,8 +715,8 @@ __device__ __forceinline__ void hist_flush(const uint32_t* __restrict__ hs, int 
 // feature into the lane's own column (bank = lane).  Reductions and shared
 // loads issue through the MIO queue, which bounds this kernel: owning two
 // features per lane spends the two loads on eight reductions instead of four.
-template <bool kGather, int kFplFull>
-__global__ void __launch_bounds__(kHistThreads, 1) hist_kernel(
+template <bool kGather, int kFplFull, int kWarps, int kStages>
+__global__ void __launch_bounds__(kWarps * 32, 1) hist_kernel(
     const uint8_t* __restrict__ bins_rm, int32_t F_pad, int32_t F, int32_t B,
     const uint4* __restrict__ qstats, const uint32_t* __restrict__ perm,
     const HistChunk* __restrict__ chunks, const uint32_t* __restrict__ n_chunks,
@@ -726,12 +724,11 @@ __global__ void __launch_bounds__(kHistThreads, 1) hist_kernel(
     extern __shared__ __align__(16) uint32_t hs[];  // table [B][4][32*fpl] then the staging ring
     const TileInfo ti = hist_tile(F, kFplFull, blockIdx.x);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    constexpr int kWarps = kHistThreads / 32;
     constexpr int kSlice = 32 * kFplFull;  // staged bytes per row
     const size_t table_words = (size_t)B * 128 * kFplFull;
-    uint8_t* sbins = (uint8_t*)(hs + table_words) + (size_t)warp * kHistStages * 32 * kSlice;
-    uint4* sstat = (uint4*)((uint8_t*)(hs + table_words) + (size_t)kWarps * kHistStages * 32 * kSlice) +
-                   (size_t)warp * kHistStages * 32;
+    uint8_t* sbins = (uint8_t*)(hs + table_words) + (size_t)warp * kStages * 32 * kSlice;
+    uint4* sstat = (uint4*)((uint8_t*)(hs + table_words) + (size_t)kWarps * kStages * 32 * kSlice) +
+                   (size_t)warp * kStages * 32;
     // 16-byte pieces of the row slice this tile needs
     const int pieces = ti.kind == 2 ? 4 : (ti.kind == 1 ? 2 : (ti.nf > 16 ? 2 : 1));
     const int narrow_w = ti.nf > 16 ? 32 : ti.nf > 8 ? 16 : ti.nf > 4 ? 8 : ti.nf > 2 ? 4 : ti.nf > 1 ? 2 : 1;
@@ -763,16 +760,16 @@ __global__ void __launch_bounds__(kHistThreads, 1) hist_kernel(
     uint32_t g = warp;
     uint32_t inext = row_of(g);
 #pragma unroll
-    for (int p = 0; p < kHistStages - 1; ++p) {
+    for (int p = 0; p < kStages - 1; ++p) {
         issue(inext, p);
         inext = row_of(g + (p + 1) * kWarps);
     }
     int st = 0;
     for (; g < n_groups; g += kWarps) {
-        // keep kHistStages - 1 groups in flight
-        issue(inext, (st + kHistStages - 1) % kHistStages);
-        inext = row_of(g + kHistStages * kWarps);
-        cp_async_wait<kHistStages - 1>();
+        // keep kStages - 1 groups in flight
+        issue(inext, (st + kStages - 1) % kStages);
+        inext = row_of(g + kStages * kWarps);
+        cp_async_wait<kStages - 1>();
         __syncwarp();
         const uint32_t cnt = len - (g << 5) < 32u ? len - (g << 5) : 32u;
         const uint8_t* sb = sbins + (size_t)st * 32 * kSlice;
@@ -780,7 +777,7 @@ __global__ void __launch_bounds__(kHistThreads, 1) hist_kernel(
         // staged rows are kSlice bytes apart; the narrow / 32-wide bodies index
         // rows 32 bytes apart, so they read the ring through a 32-byte view
         if (kFplFull == 2 && ti.kind == 2) {
-            hist_group<2, 32>(hs, sb, ss, cnt, lane, ti.nf);
+            hist_group<2, 32, true>(hs, sb, ss, cnt, lane, ti.nf);
         } else {
             // kFplFull == 2 stages 64-byte rows: re-point the row stride
             const uint8_t* sb32 = sb;
@@ -803,7 +800,7 @@ __global__ void __launch_bounds__(kHistThreads, 1) hist_kernel(
             else hist_group<1, 1>(tab, sb32, ss, cnt, lane, ti.nf);
         }
         __syncwarp();  // the stage is refilled next iteration
-        st = (st + 1) % kHistStages;
+        st = (st + 1) % kStages;
     }
     cp_async_wait<0>();
     __syncthreads();
@@ -819,13 +816,26 @@ __global__ void __launch_bounds__(kHistThreads, 1) hist_kernel(
     }
 }
 
-size_t hist_smem_bytes(int32_t B) {
-    const int fpl = hist_fpl(B);
-    return sizeof(uint32_t) * (size_t)B * 128 * fpl +
-           (size_t)(kHistThreads / 32) * kHistStages * 32 * (32 * fpl + 16);
+// Launch shapes: a lane owning two features doubles the table, so that shape
+// runs one 16-warp block per SM with a 2-deep ring; the one-feature shape
+// keeps 8-warp blocks with a 3-deep ring (two blocks per SM at 129 bins).
+struct HistShape {
+    int fpl, warps, stages;
+};
+
+static size_t hist_shape_bytes(int32_t B, const HistShape& h) {
+    return sizeof(uint32_t) * (size_t)B * 128 * h.fpl + (size_t)h.warps * h.stages * 32 * (32 * h.fpl + 16);
 }
 
-template <bool kGather, int kFpl>
+static HistShape hist_shape(int32_t B) {
+    const HistShape two{2, 16, 2};
+    if (hist_shape_bytes(B, two) <= kHistSmemMax) return two;
+    return HistShape{1, 8, 3};
+}
+
+size_t hist_smem_bytes(int32_t B) { return hist_shape_bytes(B, hist_shape(B)); }
+
+template <bool kGather, int kFpl, int kWarps, int kStages>
 static void launch_hist_variant(unsigned gy, cudaStream_t st, const uint8_t* bins_rm, int32_t F_pad, int32_t F,
                                 int32_t B, const uint4* qstats, const uint32_t* perm, const HistChunk* chunks,
                                 const uint32_t* n_chunks, ull* built) {
@@ -833,12 +843,13 @@ static void launch_hist_variant(unsigned gy, cudaStream_t st, const uint8_t* bin
     int dev = 0;
     cudaGetDevice(&dev);
     if (attr_device != dev) {
-        cudaFuncSetAttribute(hist_kernel<kGather, kFpl>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        cudaFuncSetAttribute(hist_kernel<kGather, kFpl, kWarps, kStages>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, kHistSmemMax);
         attr_device = dev;
     }
     const dim3 grid((unsigned)hist_n_tiles(F, kFpl), gy);
-    hist_kernel<kGather, kFpl><<<grid, kHistThreads, hist_smem_bytes(B), st>>>(bins_rm, F_pad, F, B, qstats,
-                                                                              perm, chunks, n_chunks, built);
+    hist_kernel<kGather, kFpl, kWarps, kStages><<<grid, kWarps * 32, hist_smem_bytes(B), st>>>(
+        bins_rm, F_pad, F, B, qstats, perm, chunks, n_chunks, built);
 }
 
 void launch_hist(const uint8_t* bins_rm, int32_t F_pad, int32_t F, int32_t B, const uint4* qstats,
@@ -846,13 +857,13 @@ void launch_hist(const uint8_t* bins_rm, int32_t F_pad, int32_t F, int32_t B, co
                  uint32_t max_chunks, ull* built, cudaStream_t st) {
     if (max_chunks == 0) return;
     const unsigned gy = max_chunks < 65535u ? max_chunks : 65535u;
-    const bool two = hist_fpl(B) == 2;
+    const bool two = hist_shape(B).fpl == 2;
     if (perm) {
-        if (two) launch_hist_variant<true, 2>(gy, st, bins_rm, F_pad, F, B, qstats, perm, chunks, n_chunks, built);
-        else launch_hist_variant<true, 1>(gy, st, bins_rm, F_pad, F, B, qstats, perm, chunks, n_chunks, built);
+        if (two) launch_hist_variant<true, 2, 16, 2>(gy, st, bins_rm, F_pad, F, B, qstats, perm, chunks, n_chunks, built);
+        else launch_hist_variant<true, 1, 8, 3>(gy, st, bins_rm, F_pad, F, B, qstats, perm, chunks, n_chunks, built);
     } else {
-        if (two) launch_hist_variant<false, 2>(gy, st, bins_rm, F_pad, F, B, qstats, perm, chunks, n_chunks, built);
-        else launch_hist_variant<false, 1>(gy, st, bins_rm, F_pad, F, B, qstats, perm, chunks, n_chunks, built);
+        if (two) launch_hist_variant<false, 2, 16, 2>(gy, st, bins_rm, F_pad, F, B, qstats, perm, chunks, n_chunks, built);
+        else launch_hist_variant<false, 1, 8, 3>(gy, st, bins_rm, F_pad, F, B, qstats, perm, chunks, n_chunks, built);
     }
 }
 

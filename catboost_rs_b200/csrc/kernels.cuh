@@ -46,9 +46,7 @@ struct TreeState {
 };
 
 constexpr int kTile = 32;          // features per histogram tile (one per lane)
-constexpr int kHistThreads = 256;  // 8 warps
-constexpr int kHistStages = 3;     // cp.async ring depth per warp (groups of 32 rows)
-constexpr int kHistMaxBinsFpl2 = 160;  // up to this many bins a lane owns 2 features (shared-memory budget)
+constexpr int kHistSmemMax = 227 * 1024;  // dynamic shared memory opt-in limit per block
 constexpr int kChunkRows = 16384;  // rows per histogram work item
 // Score-channel fixed point: |row value| <= 2^kPackBits, split at bit kPackSplit
 // into (lo, hi) u32 parts whose sums over kChunkRows rows stay below 2^31.
