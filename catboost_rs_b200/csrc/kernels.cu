@@ -623,16 +623,17 @@ __device__ __forceinline__ void hist_group(uint32_t* __restrict__ hs, const uint
                                            const uint4* __restrict__ ss, uint32_t cnt, int lane, int nf) {
     constexpr int kRows = 32 / kWt;
     constexpr int kCols = 32 * kFpl;  // u32 columns per (bin, part) row of the table
+    constexpr int kUnroll = 8;        // rows whose loads issue before their reductions
     const int sub = lane / kWt, fl = lane % kWt;
     if (!kFull && fl * kFpl >= nf) return;
     const bool second = kFull || (kFpl == 2 && fl * 2 + 1 < nf);
     uint32_t* my = hs + lane;
     uint32_t u = sub;
-    for (; u + 3 * kRows < cnt; u += 4 * kRows) {
-        uint32_t b[4][kFpl];
-        uint4 s[4];
+    for (; u + (kUnroll - 1) * kRows < cnt; u += kUnroll * kRows) {
+        uint32_t b[kUnroll][kFpl];
+        uint4 s[kUnroll];
 #pragma unroll
-        for (int v = 0; v < 4; ++v) {
+        for (int v = 0; v < kUnroll; ++v) {
             const uint32_t r = u + v * kRows;
             if (kFpl == 2) {
                 const uint32_t two = *(const uint16_t*)(sb + r * 64 + fl * 2);
@@ -644,7 +645,7 @@ __device__ __forceinline__ void hist_group(uint32_t* __restrict__ hs, const uint
             s[v] = ss[r];
         }
 #pragma unroll
-        for (int v = 0; v < 4; ++v) {
+        for (int v = 0; v < kUnroll; ++v) {
 #pragma unroll
             for (int j = 0; j < kFpl; ++j) {
                 if (j == 1 && !second) continue;
