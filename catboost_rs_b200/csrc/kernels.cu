@@ -1289,13 +1289,19 @@ __global__ void __launch_bounds__(1024) part_scan_kernel(
     }
 }
 
+// Each item's destination is computed in position order, then the tile is
+// regrouped in shared memory (the tile's false items, then its true items, each
+// in position order) so the stores of consecutive threads land on consecutive
+// destinations: a segment's false rows go to one contiguous run and its true
+// rows to another.
 __global__ void __launch_bounds__(kPartThreads) part_scatter_kernel(
     int level, int64_t n, const uint32_t* __restrict__ flags_nat,
     const uint32_t* __restrict__ perm, uint32_t* __restrict__ perm_next,
     const uint32_t* __restrict__ seg_off, const uint32_t* __restrict__ mem_start,
     const uint32_t* __restrict__ mem_leaf, const uint32_t* __restrict__ blk_off,
     const uint32_t* __restrict__ t_start, const uint32_t* __restrict__ f_cnt) {
-    __shared__ uint32_t s_idx[kPartTile];
+    __shared__ uint32_t s_idx[kPartTile];   // rows by position, then rows by regrouped slot
+    __shared__ uint32_t s_dest[kPartTile];  // destination by regrouped slot
     __shared__ uint32_t s_scan[40];
     const int K = 1 << level;
     const int64_t base = (int64_t)blockIdx.x * kPartTile;
@@ -1307,10 +1313,14 @@ __global__ void __launch_bounds__(kPartThreads) part_scatter_kernel(
     const int k0 = threadIdx.x * kPartItems;
     const int64_t j0 = base + k0;
     const int cnt_items = j0 >= n ? 0 : (int)(n - j0 < kPartItems ? n - j0 : kPartItems);
+    const int valid = (int)(n - base < kPartTile ? n - base : kPartTile);
     // all item loads issued before any is consumed (memory-level parallelism)
-    uint32_t fl_u[kPartItems];
+    uint32_t row_u[kPartItems], fl_u[kPartItems];
 #pragma unroll
-    for (int u = 0; u < kPartItems; ++u) fl_u[u] = u < cnt_items ? flag_of(flags_nat, s_idx[k0 + u]) : 0u;
+    for (int u = 0; u < kPartItems; ++u) {
+        row_u[u] = s_idx[k0 + u];
+        fl_u[u] = u < cnt_items ? flag_of(flags_nat, row_u[u]) : 0u;
+    }
     uint32_t flags = 0;
     int cnt = 0;
 #pragma unroll
@@ -1318,17 +1328,25 @@ __global__ void __launch_bounds__(kPartThreads) part_scatter_kernel(
         flags |= fl_u[u] << u;
         cnt += fl_u[u];
     }
-    const uint32_t excl = block_excl_scan<uint32_t>((uint32_t)cnt, s_scan, nullptr);
-    if (cnt_items == 0) return;
-    uint32_t T = blk_off[blockIdx.x] + excl;
-    walk_segments(mem_start, K, (uint32_t)j0, cnt_items, [&](int u, uint32_t j, int k) {
-        const uint32_t q = mem_leaf[k];
-        const uint32_t fl = (flags >> u) & 1u;
-        const uint32_t rel = T - t_start[q];
-        const uint32_t dest = fl ? seg_off[q] + f_cnt[q] + rel : j - rel;
-        perm_next[dest] = s_idx[k0 + u];
-        T += fl;
-    });
+    uint32_t tot;
+    const uint32_t excl = block_excl_scan<uint32_t>((uint32_t)cnt, s_scan, &tot);  // syncs the block
+    if (cnt_items > 0) {
+        uint32_t T = blk_off[blockIdx.x] + excl;
+        uint32_t slot_f = (uint32_t)(k0 < valid ? k0 : valid) - excl;  // false items before this thread
+        uint32_t slot_t = (uint32_t)valid - tot + excl;
+        walk_segments(mem_start, K, (uint32_t)j0, cnt_items, [&](int u, uint32_t j, int k) {
+            const uint32_t q = mem_leaf[k];
+            const uint32_t fl = (flags >> u) & 1u;
+            const uint32_t rel = T - t_start[q];
+            const uint32_t dest = fl ? seg_off[q] + f_cnt[q] + rel : j - rel;
+            const uint32_t slot = fl ? slot_t++ : slot_f++;
+            s_idx[slot] = row_u[u];
+            s_dest[slot] = dest;
+            T += fl;
+        });
+    }
+    __syncthreads();
+    for (int k = threadIdx.x; k < valid; k += blockDim.x) perm_next[s_dest[k]] = s_idx[k];
 }
 
 void launch_partition(int level, int64_t n, const uint8_t* bins_fm, int64_t n_stride,
@@ -1373,28 +1391,45 @@ void launch_small_side(int level_next, const uint32_t* child_cnt_global, uint8_t
 // leaf sums (boosting.rs:2470-2517 Gradient leaves over the full w*der1 / w
 // channels) as exact int64 sums.
 // ============================================================================
-__global__ void __launch_bounds__(kPartThreads) route_final_kernel(
-    int level, int64_t n, const uint32_t* __restrict__ flags_nat,
-    const uint32_t* __restrict__ perm, const uint32_t* __restrict__ mem_start,
-    const uint32_t* __restrict__ mem_leaf, uint16_t* __restrict__ leaf) {
-    const int K = 1 << level;
-    const int64_t j0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * kPartItems;
-    if (j0 >= n) return;
-    const int cnt = (int)(n - j0 < kPartItems ? n - j0 : kPartItems);
-    uint32_t rows[kPartItems], fl[kPartItems];
+// Final leaf id of every row in natural order, straight from the tree's splits:
+// leaf = sum over levels of (bin[f_l][i] > b_l) << l.  Each thread takes 16
+// consecutive rows: one 16-byte load per level column and two 16-byte stores.
+__global__ void __launch_bounds__(256) leaf_rows_kernel(int depth, int64_t n, const uint8_t* __restrict__ bins_fm,
+                                                        int64_t n_stride, const TreeState* __restrict__ ts,
+                                                        uint16_t* __restrict__ leaf) {
+    __shared__ PartView s_pv[16];
+    if (threadIdx.x < depth) s_pv[threadIdx.x] = part_view(ts, threadIdx.x, bins_fm, n_stride);
+    __syncthreads();
+    for (int64_t g = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; g * 16 < n;
+         g += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r0 = g * 16;
+        uint32_t lv[16];
 #pragma unroll
-    for (int u = 0; u < kPartItems; ++u)
-        rows[u] = u < cnt ? (perm ? __ldg(perm + j0 + u) : (uint32_t)(j0 + u)) : 0u;
+        for (int k = 0; k < 16; ++k) lv[k] = 0u;
+        if (r0 + 16 <= n) {
+            for (int l = 0; l < depth; ++l) {
+                const uint4 v = __ldg((const uint4*)(s_pv[l].col + r0));  // n_stride, r0 multiples of 16
+                const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+                const int32_t bl = s_pv[l].bin;
 #pragma unroll
-    for (int u = 0; u < kPartItems; ++u)
-        fl[u] = u < cnt ? flag_of(flags_nat, rows[u]) : 0u;
-    walk_segments(mem_start, K, (uint32_t)j0, cnt, [&](int u, uint32_t, int k) {
-        uint32_t i = 0, f = 0;
-#pragma unroll
-        for (int v = 0; v < kPartItems; ++v)
-            if (v == u) { i = rows[v]; f = fl[v]; }
-        leaf[i] = (uint16_t)(mem_leaf[k] | (f << level));
-    });
+                for (int k = 0; k < 16; ++k)
+                    lv[k] |= (uint32_t)((int32_t)((w[k >> 2] >> ((k & 3) * 8)) & 0xffu) > bl) << l;
+            }
+            uint4 o0, o1;
+            o0.x = lv[0] | (lv[1] << 16); o0.y = lv[2] | (lv[3] << 16);
+            o0.z = lv[4] | (lv[5] << 16); o0.w = lv[6] | (lv[7] << 16);
+            o1.x = lv[8] | (lv[9] << 16); o1.y = lv[10] | (lv[11] << 16);
+            o1.z = lv[12] | (lv[13] << 16); o1.w = lv[14] | (lv[15] << 16);
+            ((uint4*)(leaf + r0))[0] = o0;
+            ((uint4*)(leaf + r0))[1] = o1;
+        } else {
+            for (int64_t i = r0; i < n; ++i) {
+                uint32_t q = 0;
+                for (int l = 0; l < depth; ++l) q |= (uint32_t)((int32_t)s_pv[l].col[i] > s_pv[l].bin) << l;
+                leaf[i] = (uint16_t)q;
+            }
+        }
+    }
 }
 
 __global__ void __launch_bounds__(256) leafsum_kernel(int64_t n, const uint16_t* __restrict__ leaf,
@@ -1425,17 +1460,13 @@ __global__ void __launch_bounds__(256) leafsum_kernel(int64_t n, const uint16_t*
     }
 }
 
-void launch_route_leafsum(int level, int64_t n, const uint8_t* bins_fm, int64_t n_stride,
-                          const uint32_t* perm, const SegTables& sg, uint32_t* flags, uint16_t* leaf,
-                          const double* wd1, const double* weight, int depth, TreeState* ts, ull* leaf_sums,
+void launch_route_leafsum(int depth, int64_t n, const uint8_t* bins_fm, int64_t n_stride, uint16_t* leaf,
+                          const double* wd1, const double* weight, TreeState* ts, ull* leaf_sums,
                           cudaStream_t st) {
     if (n <= 0) return;
-    const int64_t words = (n + 31) >> 5;
-    split_flags_kernel<<<(unsigned)std::min<int64_t>((words + 255) / 256, 148 * 8), 256, 0, st>>>(
-        level, n, bins_fm, n_stride, ts, flags);
-    const int64_t threads = (n + kPartItems - 1) / kPartItems;
-    route_final_kernel<<<(unsigned)((threads + kPartThreads - 1) / kPartThreads), kPartThreads, 0, st>>>(
-        level, n, flags, perm, sg.mem_start, sg.mem_leaf, leaf);
+    const int64_t groups = (n + 15) / 16;
+    leaf_rows_kernel<<<(unsigned)std::min<int64_t>((groups + 255) / 256, 148 * 8), 256, 0, st>>>(
+        depth, n, bins_fm, n_stride, ts, leaf);
     int64_t blocks = (n + 255) / 256;
     if (blocks > 148 * 4) blocks = 148 * 4;
     const size_t smem = depth <= 10 ? sizeof(ull) * 2 * (1 << depth) : 0;

@@ -123,9 +123,8 @@ void launch_partition(int level, int64_t n, const uint8_t* bins_fm, int64_t n_st
                       uint32_t* flags, uint32_t* child_cnt, TreeState* ts, cudaStream_t st);
 void launch_small_side(int level_next, const uint32_t* child_cnt_global, uint8_t* small_side,
                        cudaStream_t st);
-void launch_route_leafsum(int level, int64_t n, const uint8_t* bins_fm, int64_t n_stride,
-                          const uint32_t* perm, const SegTables& sg, uint32_t* flags, uint16_t* leaf,
-                          const double* wd1, const double* weight, int depth, TreeState* ts, ull* leaf_sums,
+void launch_route_leafsum(int depth, int64_t n, const uint8_t* bins_fm, int64_t n_stride, uint16_t* leaf,
+                          const double* wd1, const double* weight, TreeState* ts, ull* leaf_sums,
                           cudaStream_t st);
 void launch_leaf_values(int depth, int n_splits_expected, const ull* leaf_sums, double l2, double lr,
                         TreeState* ts, double* leaf_raw, double* leaf_lrv, cudaStream_t st);

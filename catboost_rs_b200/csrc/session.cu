@@ -545,9 +545,9 @@ int grow(cbgpu_session* s, const double* approx_h, const double* target_h, int64
             launches += 5;
         } else {
             CU(cudaMemsetAsync(s->leaf_sums, 0, sizeof(ull) * 2 * L, st));
-            launch_route_leafsum(l, s->n, s->bins_fm, s->n_stride, l == 0 ? nullptr : s->perm[pp], s->sg,
-                                 s->flags, s->leaf, s->wd1, s->weight, D, s->ts, s->leaf_sums, st);
-            launches += 3;
+            launch_route_leafsum(D, s->n, s->bins_fm, s->n_stride, s->leaf, s->wd1, s->weight, s->ts,
+                                 s->leaf_sums, st);
+            launches += 2;
             rec(e + 4);
             int rc = allreduce(s, s->leaf_sums, (size_t)2 * L, ncclUint64, ncclSum);
             if (rc) return rc;
