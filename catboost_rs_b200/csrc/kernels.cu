@@ -950,33 +950,26 @@ __global__ void derive_prefix_kernel(int level, int32_t F, int32_t B, const ull*
         p = q & (half - 1);
         is_built = ((q >> (level - 1)) & 1) == (int64_t)small_side[p];
     }
-    const ull* src = built + ((size_t)p * F + f) * B * 2;
-    const ull* par = (level > 0) ? prev + ((size_t)p * F + f) * B * 2 : nullptr;
-    ull* dst = cur + ((size_t)q * F + f) * B * 2;
-    const int K = (B + 31) / 32;
-    const int b0 = lane * K;
-    long long lg = 0, lh = 0;
-    for (int k = 0; k < K; ++k) {
-        int b = b0 + k;
+    const ulonglong2* src = (const ulonglong2*)(built + ((size_t)p * F + f) * B * 2);
+    const ulonglong2* par = (level > 0) ? (const ulonglong2*)(prev + ((size_t)p * F + f) * B * 2) : nullptr;
+    ulonglong2* dst = (ulonglong2*)(cur + ((size_t)q * F + f) * B * 2);
+    // bins b = 32k + lane: coalesced 16-byte (g, h) pairs, prefix carried across rounds
+    long long cg = 0, ch = 0;
+    for (int b0 = 0; b0 < B; b0 += 32) {
+        const int b = b0 + lane;
+        ulonglong2 v = make_ulonglong2(0ull, 0ull);
+        if (b < B) v = src[b];
+        const long long ig = warp_incl_scan<long long>((long long)v.x) + cg;
+        const long long ih = warp_incl_scan<long long>((long long)v.y) + ch;
+        cg = __shfl_sync(kFull, ig, 31);
+        ch = __shfl_sync(kFull, ih, 31);
         if (b < B) {
-            lg += (long long)src[2 * b];
-            lh += (long long)src[2 * b + 1];
-        }
-    }
-    long long ig = warp_incl_scan<long long>(lg), ih = warp_incl_scan<long long>(lh);
-    long long ag = ig - lg, ah = ih - lh;
-    for (int k = 0; k < K; ++k) {
-        int b = b0 + k;
-        if (b < B) {
-            ag += (long long)src[2 * b];
-            ah += (long long)src[2 * b + 1];
-            long long og = ag, oh = ah;
+            ulonglong2 o = make_ulonglong2((ull)ig, (ull)ih);
             if (!is_built) {
-                og = (long long)par[2 * b] - ag;
-                oh = (long long)par[2 * b + 1] - ah;
+                const ulonglong2 pv = par[b];
+                o = make_ulonglong2((ull)((long long)pv.x - ig), (ull)((long long)pv.y - ih));
             }
-            dst[2 * b] = (ull)og;
-            dst[2 * b + 1] = (ull)oh;
+            dst[b] = o;
         }
     }
 }
@@ -990,16 +983,25 @@ void launch_derive_prefix(int level, int32_t F, int32_t B, const ull* built, con
 
 // ============================================================================
 // scoring (score.rs:39-265, histogram.rs:1007-1171) + argmax (tree.rs:355-366)
-// One block per feature, one thread per candidate border; the 2Q children are
-// folded in the CPU's canonical order (false children 0..Q-1, then true).
+// One block per feature.  The per-child terms avg*swd and avg^2*sw of every
+// (child, border) pair are independent, so the block computes a piece of
+// kScorePiece children for all borders at once into shared memory; then one
+// thread per border adds them to its running sums in the CPU's canonical order
+// (false children 0..Q-1, then true), so the sums round as the CPU's do.
 // The last block to finish reduces the per-feature winners (no spin wait).
 // ============================================================================
-__global__ void __launch_bounds__(128) score_kernel(int level, int32_t F, int32_t B,
+constexpr int kScoreThreads = 256;
+constexpr int kScorePiece = 8;     // children per piece
+constexpr int kScoreMaxBorders = 256;
+
+__global__ void __launch_bounds__(kScoreThreads) score_kernel(int level, int32_t F, int32_t B,
                                                     const ull* __restrict__ cur,
                                                     const int32_t* __restrict__ border_counts,
                                                     double l2, int score_fn,
                                                     double* __restrict__ feat_score,
                                                     int32_t* __restrict__ feat_bin, TreeState* ts) {
+    __shared__ double s_num[kScorePiece][kScoreMaxBorders];
+    __shared__ double s_den[kScorePiece][kScoreMaxBorders];
     __shared__ double s_sc[32];
     __shared__ int s_bi[32];
     __shared__ bool s_last;
@@ -1007,30 +1009,52 @@ __global__ void __launch_bounds__(128) score_kernel(int level, int32_t F, int32_
     const int nb = border_counts[f];
     const int Q = 1 << level;
     const double ig = ts->sc.inv[0], ih = ts->sc.inv[1];
-    double best = -INFINITY;
-    int bbin = 0x7fffffff;
-    for (int b = threadIdx.x; b < nb; b += blockDim.x) {
-        double num = 0.0, den = 1e-100;
-        for (int side = 0; side < 2; ++side) {
-            for (int q = 0; q < Q; ++q) {
-                const ull* row = cur + ((size_t)q * F + f) * B * 2;
-                long long pg = (long long)row[2 * b], ph = (long long)row[2 * b + 1];
-                if (side) {
-                    pg = (long long)row[2 * (B - 1)] - pg;
-                    ph = (long long)row[2 * (B - 1) + 1] - ph;
+    // running sums of the border this thread owns (b = threadIdx.x, and
+    // b + kScoreThreads when nb > kScoreThreads; nb <= kScoreMaxBorders)
+    double num[2] = {0.0, 0.0}, den[2] = {1e-100, 1e-100};
+    for (int c0 = 0; c0 < 2 * Q; c0 += kScorePiece) {
+        const int pc = 2 * Q - c0 < kScorePiece ? 2 * Q - c0 : kScorePiece;
+        for (int t = threadIdx.x; t < pc * nb; t += blockDim.x) {
+            const int cc = t / nb, b = t - cc * nb;
+            const int ch = c0 + cc;  // canonical child index: side * Q + q
+            const int side = ch >= Q, q = ch - side * Q;
+            const ull* row = cur + ((size_t)q * F + f) * B * 2;
+            long long pg = (long long)row[2 * b], ph = (long long)row[2 * b + 1];
+            if (side) {
+                pg = (long long)row[2 * (B - 1)] - pg;
+                ph = (long long)row[2 * (B - 1) + 1] - ph;
+            }
+            const double swd = __dmul_rn((double)pg, ig);
+            const double sw = __dmul_rn((double)ph, ih);
+            const double avg = sw > 0.0 ? __ddiv_rn(swd, __dadd_rn(sw, l2)) : 0.0;
+            s_num[cc][b] = __dmul_rn(avg, swd);
+            s_den[cc][b] = __dmul_rn(__dmul_rn(avg, avg), sw);
+        }
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const int b = threadIdx.x + k * kScoreThreads;
+            if (b < nb) {
+                for (int cc = 0; cc < pc; ++cc) {
+                    num[k] = __dadd_rn(num[k], s_num[cc][b]);
+                    if (score_fn == 0) den[k] = __dadd_rn(den[k], s_den[cc][b]);
                 }
-                const double swd = __dmul_rn((double)pg, ig);
-                const double sw = __dmul_rn((double)ph, ih);
-                const double avg = sw > 0.0 ? __ddiv_rn(swd, __dadd_rn(sw, l2)) : 0.0;
-                num = __dadd_rn(num, __dmul_rn(avg, swd));
-                if (score_fn == 0) den = __dadd_rn(den, __dmul_rn(__dmul_rn(avg, avg), sw));
             }
         }
-        double s = score_fn == 0 ? __ddiv_rn(num, sqrt(den)) : num;
-        s = nan_to_neg_inf(s);
-        if (better(s, b, best, bbin)) {
-            best = s;
-            bbin = b;
+        __syncthreads();
+    }
+    double best = -INFINITY;
+    int bbin = 0x7fffffff;
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        const int b = threadIdx.x + k * kScoreThreads;
+        if (b < nb) {
+            double s = score_fn == 0 ? __ddiv_rn(num[k], sqrt(den[k])) : num[k];
+            s = nan_to_neg_inf(s);
+            if (better(s, b, best, bbin)) {
+                best = s;
+                bbin = b;
+            }
         }
     }
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
@@ -1091,7 +1115,7 @@ __global__ void __launch_bounds__(128) score_kernel(int level, int32_t F, int32_
 void launch_score(int level, int32_t F, int32_t B, const ull* cur, const int32_t* border_counts,
                   double l2, int score_fn, double* feat_score, int32_t* feat_bin, TreeState* ts,
                   cudaStream_t st) {
-    score_kernel<<<(unsigned)F, 128, 0, st>>>(level, F, B, cur, border_counts, l2, score_fn,
+    score_kernel<<<(unsigned)F, kScoreThreads, 0, st>>>(level, F, B, cur, border_counts, l2, score_fn,
                                               feat_score, feat_bin, ts);
 }
 
