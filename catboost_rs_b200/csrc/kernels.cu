@@ -1208,55 +1208,96 @@ __device__ __forceinline__ uint32_t flag_of(const uint32_t* __restrict__ flags, 
     return (__ldg(flags + (i >> 5)) >> (i & 31)) & 1u;
 }
 
+// Positions are processed warp-striped: warp w of a tile owns kPartRounds
+// rounds of 32 consecutive positions, lane = position within the round, so
+// row-order loads are coalesced and each round's outcome is one ballot word
+// (bit lane of word j / 32 = outcome of position j).  A position's in-tile
+// true prefix is the prefix of the tile's word popcounts plus a masked popc.
+constexpr int kPartWords = kPartTile / 32;
+constexpr int kPartRounds = kPartWords / (kPartThreads / 32);
+
+// Exclusive prefix of the popcounts of the tile's kPartWords ballot words
+// (warp 0; kPartWords = 4 x 32).  Returns the tile total to every thread of warp 0.
+__device__ __forceinline__ uint32_t tile_word_prefix(const uint32_t* __restrict__ s_w, uint32_t* __restrict__ s_pre) {
+    static_assert(kPartWords == 128, "tile prefix assumes 4 words per lane");
+    const int lane = threadIdx.x & 31;
+    uint32_t c[4], t = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        c[i] = (uint32_t)__popc(s_w[4 * lane + i]);
+        t += c[i];
+    }
+    const uint32_t inc = warp_incl_scan<uint32_t>(t);
+    uint32_t run = inc - t;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        s_pre[4 * lane + i] = run;
+        run += c[i];
+    }
+    return __shfl_sync(kFull, inc, 31);
+}
+
+__device__ __forceinline__ uint32_t tile_prefix_at(const uint32_t* s_w, const uint32_t* s_pre, uint32_t p) {
+    return s_pre[p >> 5] + (uint32_t)__popc(s_w[p >> 5] & ((1u << (p & 31)) - 1u));
+}
+
 __global__ void __launch_bounds__(kPartThreads) part_count_kernel(
-    int level, int64_t n, const uint32_t* __restrict__ flags_nat, const uint32_t* __restrict__ perm, const uint32_t* __restrict__ seg_cnt,
+    int level, int64_t n, const uint32_t* __restrict__ flags_nat, const uint32_t* __restrict__ perm,
+    uint32_t* __restrict__ flags_pos, const uint32_t* __restrict__ seg_cnt,
     const uint32_t* __restrict__ mem_start, const uint32_t* __restrict__ mem_leaf,
     uint32_t* __restrict__ seg_start_blk, uint32_t* __restrict__ seg_start_part,
     uint32_t* __restrict__ seg_end_blk, uint32_t* __restrict__ seg_end_part,
     uint32_t* __restrict__ blk_true) {
-    __shared__ uint32_t s_idx[kPartTile];
-    __shared__ uint32_t s_scan[40];
-    const int K = 1 << level;
+    __shared__ uint32_t s_w[kPartWords];
+    __shared__ uint32_t s_pre[kPartWords];
+    __shared__ uint32_t s_tot;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int64_t base = (int64_t)blockIdx.x * kPartTile;
-    for (int k = threadIdx.x; k < kPartTile; k += blockDim.x) {
-        int64_t j = base + k;
-        s_idx[k] = j < n ? (perm ? perm[j] : (uint32_t)j) : 0xffffffffu;
+    const int64_t pw = base + (int64_t)warp * kPartRounds * 32;  // first position of this warp
+    // all row and flag loads issued before any is consumed (memory-level parallelism)
+    uint32_t row[kPartRounds], fl[kPartRounds];
+#pragma unroll
+    for (int r = 0; r < kPartRounds; ++r) {
+        const int64_t j = pw + r * 32 + lane;
+        row[r] = j < n ? (perm ? __ldg(perm + j) : (uint32_t)j) : 0xffffffffu;
+    }
+#pragma unroll
+    for (int r = 0; r < kPartRounds; ++r) fl[r] = row[r] != 0xffffffffu ? flag_of(flags_nat, row[r]) : 0u;
+#pragma unroll
+    for (int r = 0; r < kPartRounds; ++r) {
+        const uint32_t m = __ballot_sync(kFull, fl[r] != 0u);
+        if (lane == 0) {
+            s_w[warp * kPartRounds + r] = m;
+            if (pw + r * 32 < n) flags_pos[(pw >> 5) + r] = m;
+        }
     }
     __syncthreads();
-    const int k0 = threadIdx.x * kPartItems;
-    const int64_t j0 = base + k0;
-    const int cnt_items = j0 >= n ? 0 : (int)(n - j0 < kPartItems ? n - j0 : kPartItems);
-    // all item loads issued before any is consumed (memory-level parallelism)
-    uint32_t fl_u[kPartItems];
-#pragma unroll
-    for (int u = 0; u < kPartItems; ++u) fl_u[u] = u < cnt_items ? flag_of(flags_nat, s_idx[k0 + u]) : 0u;
-    uint32_t flags = 0;
-    int cnt = 0;
-#pragma unroll
-    for (int u = 0; u < kPartItems; ++u) {
-        flags |= fl_u[u] << u;
-        cnt += fl_u[u];
+    if (warp == 0) {
+        const uint32_t tot = tile_word_prefix(s_w, s_pre);
+        if (lane == 0) s_tot = tot;
     }
-    uint32_t tot;
-    const uint32_t excl = block_excl_scan<uint32_t>((uint32_t)cnt, s_scan, &tot);
-    if (cnt_items > 0) {
-        uint32_t run = excl;
-        walk_segments(mem_start, K, (uint32_t)j0, cnt_items, [&](int u, uint32_t j, int k) {
-            const uint32_t q = mem_leaf[k];
-            const uint32_t s0 = mem_start[k];
-            const uint32_t fl = (flags >> u) & 1u;
-            if (j == s0) {
-                seg_start_blk[q] = blockIdx.x;
-                seg_start_part[q] = run;
-            }
-            run += fl;
-            if (j == s0 + seg_cnt[q] - 1) {
-                seg_end_blk[q] = blockIdx.x;
-                seg_end_part[q] = run;
-            }
-        });
+    __syncthreads();
+    // segment starts / ends inside the tile: their exclusive / inclusive in-tile prefixes
+    const int K = 1 << level;
+    const int64_t tile_end = base + kPartTile < n ? base + kPartTile : n;
+    const int k_first = seg_of(mem_start, K, (uint32_t)base);
+    const int k_last = seg_of(mem_start, K, (uint32_t)(tile_end - 1));
+    for (int k = k_first + threadIdx.x; k <= k_last; k += blockDim.x) {
+        const uint32_t q = mem_leaf[k];
+        const uint32_t cnt = seg_cnt[q];
+        if (cnt == 0) continue;
+        const int64_t s0 = mem_start[k], e = s0 + cnt - 1;
+        if (s0 >= base && s0 < tile_end) {
+            seg_start_blk[q] = blockIdx.x;
+            seg_start_part[q] = tile_prefix_at(s_w, s_pre, (uint32_t)(s0 - base));
+        }
+        if (e >= base && e < tile_end) {
+            const uint32_t p = (uint32_t)(e - base);
+            seg_end_blk[q] = blockIdx.x;
+            seg_end_part[q] = tile_prefix_at(s_w, s_pre, p) + ((s_w[p >> 5] >> (p & 31)) & 1u);
+        }
     }
-    if (threadIdx.x == 0) blk_true[blockIdx.x] = tot;
+    if (threadIdx.x == 0) blk_true[blockIdx.x] = s_tot;
 }
 
 __global__ void __launch_bounds__(1024) part_scan_kernel(
@@ -1313,64 +1354,56 @@ __global__ void __launch_bounds__(1024) part_scan_kernel(
     }
 }
 
-// Each item's destination is computed in position order, then the tile is
-// regrouped in shared memory (the tile's false items, then its true items, each
-// in position order) so the stores of consecutive threads land on consecutive
-// destinations: a segment's false rows go to one contiguous run and its true
-// rows to another.
+// Destinations: a false position j of segment q goes to j - (trues before it
+// in q), a true one to seg_off[q] + f_cnt[q] + (trues before it in q); within a
+// round the false lanes and the true lanes each store to one contiguous run.
 __global__ void __launch_bounds__(kPartThreads) part_scatter_kernel(
-    int level, int64_t n, const uint32_t* __restrict__ flags_nat,
+    int level, int64_t n, const uint32_t* __restrict__ flags_pos,
     const uint32_t* __restrict__ perm, uint32_t* __restrict__ perm_next,
     const uint32_t* __restrict__ seg_off, const uint32_t* __restrict__ mem_start,
     const uint32_t* __restrict__ mem_leaf, const uint32_t* __restrict__ blk_off,
     const uint32_t* __restrict__ t_start, const uint32_t* __restrict__ f_cnt) {
-    __shared__ uint32_t s_idx[kPartTile];   // rows by position, then rows by regrouped slot
-    __shared__ uint32_t s_dest[kPartTile];  // destination by regrouped slot
-    __shared__ uint32_t s_scan[40];
-    const int K = 1 << level;
+    __shared__ uint32_t s_w[kPartWords];
+    __shared__ uint32_t s_pre[kPartWords];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int64_t base = (int64_t)blockIdx.x * kPartTile;
-    for (int k = threadIdx.x; k < kPartTile; k += blockDim.x) {
-        int64_t j = base + k;
-        s_idx[k] = j < n ? (perm ? perm[j] : (uint32_t)j) : 0xffffffffu;
+    const int64_t words = (n + 31) >> 5;
+    for (int k = threadIdx.x; k < kPartWords; k += blockDim.x) {
+        const int64_t w = (base >> 5) + k;
+        s_w[k] = w < words ? flags_pos[w] : 0u;
+    }
+    const int64_t pw = base + (int64_t)warp * kPartRounds * 32;
+    uint32_t row[kPartRounds];
+#pragma unroll
+    for (int r = 0; r < kPartRounds; ++r) {
+        const int64_t j = pw + r * 32 + lane;
+        row[r] = j < n ? (perm ? __ldg(perm + j) : (uint32_t)j) : 0u;
     }
     __syncthreads();
-    const int k0 = threadIdx.x * kPartItems;
-    const int64_t j0 = base + k0;
-    const int cnt_items = j0 >= n ? 0 : (int)(n - j0 < kPartItems ? n - j0 : kPartItems);
-    const int valid = (int)(n - base < kPartTile ? n - base : kPartTile);
-    // all item loads issued before any is consumed (memory-level parallelism)
-    uint32_t row_u[kPartItems], fl_u[kPartItems];
+    if (warp == 0) (void)tile_word_prefix(s_w, s_pre);
+    __syncthreads();
+    if (pw >= n) return;
+    const int K = 1 << level;
+    const uint32_t t0 = blk_off[blockIdx.x];
+    int k = seg_of(mem_start, K, (uint32_t)pw);
+    const uint32_t lt = (1u << lane) - 1u;
 #pragma unroll
-    for (int u = 0; u < kPartItems; ++u) {
-        row_u[u] = s_idx[k0 + u];
-        fl_u[u] = u < cnt_items ? flag_of(flags_nat, row_u[u]) : 0u;
-    }
-    uint32_t flags = 0;
-    int cnt = 0;
-#pragma unroll
-    for (int u = 0; u < kPartItems; ++u) {
-        flags |= fl_u[u] << u;
-        cnt += fl_u[u];
-    }
-    uint32_t tot;
-    const uint32_t excl = block_excl_scan<uint32_t>((uint32_t)cnt, s_scan, &tot);  // syncs the block
-    if (cnt_items > 0) {
-        uint32_t T = blk_off[blockIdx.x] + excl;
-        uint32_t slot_f = (uint32_t)(k0 < valid ? k0 : valid) - excl;  // false items before this thread
-        uint32_t slot_t = (uint32_t)valid - tot + excl;
-        walk_segments(mem_start, K, (uint32_t)j0, cnt_items, [&](int u, uint32_t j, int k) {
-            const uint32_t q = mem_leaf[k];
-            const uint32_t fl = (flags >> u) & 1u;
+    for (int r = 0; r < kPartRounds; ++r) {
+        const int64_t j = pw + r * 32 + lane;
+        int kl = k;
+        while (kl + 1 < K && (int64_t)mem_start[kl + 1] <= j) ++kl;
+        k = __shfl_sync(kFull, kl, 31);
+        const int wi = warp * kPartRounds + r;
+        const uint32_t m = s_w[wi];
+        const uint32_t fl = (m >> lane) & 1u;
+        const uint32_t T = t0 + s_pre[wi] + (uint32_t)__popc(m & lt);
+        if (j < n) {
+            const uint32_t q = mem_leaf[kl];
             const uint32_t rel = T - t_start[q];
-            const uint32_t dest = fl ? seg_off[q] + f_cnt[q] + rel : j - rel;
-            const uint32_t slot = fl ? slot_t++ : slot_f++;
-            s_idx[slot] = row_u[u];
-            s_dest[slot] = dest;
-            T += fl;
-        });
+            const uint32_t dest = fl ? seg_off[q] + f_cnt[q] + rel : (uint32_t)j - rel;
+            perm_next[dest] = row[r];
+        }
     }
-    __syncthreads();
-    for (int k = threadIdx.x; k < valid; k += blockDim.x) perm_next[s_dest[k]] = s_idx[k];
 }
 
 void launch_partition(int level, int64_t n, const uint8_t* bins_fm, int64_t n_stride,
@@ -1381,14 +1414,15 @@ void launch_partition(int level, int64_t n, const uint8_t* bins_fm, int64_t n_st
     const int64_t words = (n + 31) >> 5;
     split_flags_kernel<<<(unsigned)std::min<int64_t>((words + 255) / 256, 148 * 8), 256, 0, st>>>(
         level, n, bins_fm, n_stride, ts, flags);
-    part_count_kernel<<<tiles, kPartThreads, 0, st>>>(level, n, flags, perm, sg.seg_cnt, sg.mem_start,
+    uint32_t* flags_pos = flags + words + 1;  // position-order outcome words
+    part_count_kernel<<<tiles, kPartThreads, 0, st>>>(level, n, flags, perm, flags_pos, sg.seg_cnt, sg.mem_start,
                                                        sg.mem_leaf, sg.start_blk, sg.start_part, sg.end_blk,
                                                        sg.end_part, blk_true);
     part_scan_kernel<<<1, 1024, 0, st>>>(level, tiles, blk_true, sg.seg_off, sg.seg_cnt, sg.mem_leaf,
                                          sg.start_blk, sg.start_part, sg.end_blk, sg.end_part, sg.t_start,
                                          sg.f_cnt, child_cnt, sg.seg_off_next, sg.seg_cnt_next,
                                          sg.mem_start_next, sg.mem_leaf_next);
-    part_scatter_kernel<<<tiles, kPartThreads, 0, st>>>(level, n, flags, perm, perm_next, sg.seg_off,
+    part_scatter_kernel<<<tiles, kPartThreads, 0, st>>>(level, n, flags_pos, perm, perm_next, sg.seg_off,
                                                          sg.mem_start, sg.mem_leaf, blk_true, sg.t_start,
                                                          sg.f_cnt);
     sg.swap();

@@ -117,7 +117,7 @@ void launch_derive_prefix(int level, int32_t F, int32_t B, const ull* built, con
 void launch_score(int level, int32_t F, int32_t B, const ull* cur, const int32_t* border_counts,
                   double l2, int score_fn, double* feat_score, int32_t* feat_bin, TreeState* ts,
                   cudaStream_t st);
-// flags: ceil(n / 32) words (the split outcome bits); blk_true: ceil(n / kPartTile) + 1; child_cnt: 2^(level+1) (false counts, then true).
+// flags: 2 * (ceil(n / 32) + 1) words (the split outcome bits, natural then position order); blk_true: ceil(n / kPartTile) + 1; child_cnt: 2^(level+1) (false counts, then true).
 void launch_partition(int level, int64_t n, const uint8_t* bins_fm, int64_t n_stride,
                       const uint32_t* perm, uint32_t* perm_next, SegTables& sg, uint32_t* blk_true,
                       uint32_t* flags, uint32_t* child_cnt, TreeState* ts, cudaStream_t st);

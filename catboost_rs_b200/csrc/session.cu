@@ -263,7 +263,7 @@ int alloc_session(cbgpu_session* s, const cbgpu_begin_args* a) {
     }
     DA(s->blk_true, (n + kPartTile - 1) / kPartTile + 1);
     DA(s->child_cnt, 1 << 17);
-    DA(s->flags, (n + 31) / 32 + 1);
+    DA(s->flags, 2 * ((n + 31) / 32 + 1));  // natural-order outcome bits, then position-order words
     DA(s->small_side, 1 << 16);
     const size_t max_chunks = (size_t)(n / kChunkRows) + (L / 2) + 2;
     DA(s->chunks, max_chunks);
