@@ -180,25 +180,35 @@ void launch_transpose_rm_to_fm(const uint8_t* rm, int64_t n, int32_t F, int32_t 
 // jumps once and steps kBootRun consecutive rows.
 __global__ void bootstrap_kernel(int mode, int64_t n, int64_t row_offset, uint64_t rand_seed,
                                  Rng64 base, double rate, float temp, float* __restrict__ out) {
+    static_assert(kBootRun == 8, "a run is stored as two float4");
     int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
     int64_t i0 = t * kBootRun;
     if (i0 >= n) return;
     int64_t g0 = row_offset + i0;
+    float v[kBootRun];
     if (mode == 1) {
         Rng64 r = Rng64::from_seed(rand_seed + (uint64_t)(g0 / 1000));
         r.advance(10 + (uint64_t)(g0 % 1000));
-        for (int j = 0; j < kBootRun && i0 + j < n; ++j) {
+#pragma unroll
+        for (int j = 0; j < kBootRun; ++j) {
             int64_t g = g0 + j;
             if (j > 0 && g % 1000 == 0) {
                 r = Rng64::from_seed(rand_seed + (uint64_t)(g / 1000));
                 r.advance(10);
             }
-            out[i0 + j] = (float)bayesian_weight(real1(r), temp);
+            v[j] = i0 + j < n ? (float)bayesian_weight(real1(r), temp) : 0.0f;
         }
     } else {
         Rng64 r = base;
         r.advance((uint64_t)g0);
-        for (int j = 0; j < kBootRun && i0 + j < n; ++j) out[i0 + j] = real1(r) < rate ? 1.0f : 0.0f;
+#pragma unroll
+        for (int j = 0; j < kBootRun; ++j) v[j] = i0 + j < n && real1(r) < rate ? 1.0f : 0.0f;
+    }
+    if (i0 + kBootRun <= n) {  // i0 is a multiple of 8 floats: 32-byte aligned
+        ((float4*)(out + i0))[0] = make_float4(v[0], v[1], v[2], v[3]);
+        ((float4*)(out + i0))[1] = make_float4(v[4], v[5], v[6], v[7]);
+    } else {
+        for (int j = 0; i0 + j < n; ++j) out[i0 + j] = v[j];
     }
 }
 
@@ -410,6 +420,15 @@ __device__ __forceinline__ double sample_of(int s_mode, const float* sw32, const
 // approx += lr * leaf value of the previous tree (when pending), then
 // der1 (RMSE t - a; Logloss t - (1 - 1/(1 + e^a))), wd1 = der1 * w, and the
 // maxima of |g| = |wd1 * s|, |h| = |w * s|, |wd1|, |w| for the fixed-point scales.
+__device__ __forceinline__ double der1_of(int loss, double a, double t) {
+    if (loss == 0) return __dsub_rn(t, a);
+    const double e = exp(a);
+    const double p = __dsub_rn(1.0, __ddiv_rn(1.0, __dadd_rn(1.0, e)));
+    return __dsub_rn(t, p);
+}
+
+constexpr int kDerRows = 4;  // rows per thread per step, loads issued first
+
 __global__ void __launch_bounds__(256) der_kernel(
     int64_t n, int loss, double* __restrict__ approx, const double* __restrict__ target,
     const double* __restrict__ weight, const uint16_t* __restrict__ leaf,
@@ -417,34 +436,37 @@ __global__ void __launch_bounds__(256) der_kernel(
     const double* __restrict__ sw64, double* __restrict__ wd1, TreeState* ts, bool defer) {
     double m[4] = {0.0, 0.0, 0.0, 0.0};
     bool bad = false;
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        double a = approx[i];
-        if (lrv) {
-            a = __dadd_rn(a, lrv[leaf[i]]);
-            approx[i] = a;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i0 < n; i0 += stride * kDerRows) {
+        double a[kDerRows], t[kDerRows], w[kDerRows], sv[kDerRows];
+#pragma unroll
+        for (int k = 0; k < kDerRows; ++k) {
+            const int64_t i = i0 + k * stride;
+            a[k] = 0.0; t[k] = 0.0; w[k] = 1.0; sv[k] = 1.0;
+            if (i < n) {
+                a[k] = approx[i];
+                if (lrv) a[k] = __dadd_rn(a[k], lrv[leaf[i]]);
+                t[k] = target[i];
+                if (weight) w[k] = weight[i];
+                if (!defer) sv[k] = sample_of(s_mode, sw32, sw64, i);
+            }
         }
-        const double t = target[i];
-        double d1;
-        if (loss == 0) {
-            d1 = __dsub_rn(t, a);
-        } else {
-            const double e = exp(a);
-            const double p = __dsub_rn(1.0, __ddiv_rn(1.0, __dadd_rn(1.0, e)));
-            d1 = __dsub_rn(t, p);
-        }
-        const double w = weight ? weight[i] : 1.0;
-        const double wd = __dmul_rn(d1, w);
-        wd1[i] = wd;
-        m[2] = fmax(m[2], fabs(wd));
-        m[3] = fmax(m[3], fabs(w));
-        bad |= !isfinite(wd);
-        if (!defer) {
-            const double s = sample_of(s_mode, sw32, sw64, i);
-            const double g = __dmul_rn(wd, s), h = __dmul_rn(w, s);
-            m[0] = fmax(m[0], fabs(g));
-            m[1] = fmax(m[1], fabs(h));
-            bad |= !isfinite(g) || !isfinite(h);
+#pragma unroll
+        for (int k = 0; k < kDerRows; ++k) {
+            const int64_t i = i0 + k * stride;
+            if (i >= n) continue;
+            if (lrv) approx[i] = a[k];
+            const double wd = __dmul_rn(der1_of(loss, a[k], t[k]), w[k]);
+            wd1[i] = wd;
+            m[2] = fmax(m[2], fabs(wd));
+            m[3] = fmax(m[3], fabs(w[k]));
+            bad |= !isfinite(wd);
+            if (!defer) {
+                const double g = __dmul_rn(wd, sv[k]), h = __dmul_rn(w[k], sv[k]);
+                m[0] = fmax(m[0], fabs(g));
+                m[1] = fmax(m[1], fabs(h));
+                bad |= !isfinite(g) || !isfinite(h);
+            }
         }
     }
     if (bad) atomicOr(&ts->err, kErrOverflow);
@@ -983,128 +1005,136 @@ void launch_derive_prefix(int level, int32_t F, int32_t B, const ull* built, con
 
 // ============================================================================
 // scoring (score.rs:39-265, histogram.rs:1007-1171) + argmax (tree.rs:355-366)
-// One block per feature.  The per-child terms avg*swd and avg^2*sw of every
-// (child, border) pair are independent, so the block computes a piece of
-// kScorePiece children for all borders at once into shared memory; then one
-// thread per border adds them to its running sums in the CPU's canonical order
-// (false children 0..Q-1, then true), so the sums round as the CPU's do.
-// The last block to finish reduces the per-feature winners (no spin wait).
+// Block (border group g, feature f) scores up to 32 consecutive borders
+// (lane = border, so the (g, h) pairs of a child load as one 512-byte run).
+// The per-child terms avg*swd and avg^2*sw are independent, so the 8 warps
+// compute a piece of kScorePiece children into shared memory; then warp 0 adds
+// them to each border's running sums in the CPU's canonical order (false
+// children 0..Q-1, then true), so the sums round as the CPU's do.  The last
+// block to finish reduces the per-group winners in (feature, border) order,
+// which is the CPU's first-wins strict-> scan (no spin wait).
 // ============================================================================
-constexpr int kScoreThreads = 256;
-constexpr int kScorePiece = 8;     // children per piece
-constexpr int kScoreMaxBorders = 256;
+constexpr int kScoreWarps = 8;
+constexpr int kScorePiece = 64;  // children per piece, kScorePiece / kScoreWarps per warp
 
-__global__ void __launch_bounds__(kScoreThreads) score_kernel(int level, int32_t F, int32_t B,
-                                                    const ull* __restrict__ cur,
-                                                    const int32_t* __restrict__ border_counts,
-                                                    double l2, int score_fn,
-                                                    double* __restrict__ feat_score,
-                                                    int32_t* __restrict__ feat_bin, TreeState* ts) {
-    __shared__ double s_num[kScorePiece][kScoreMaxBorders];
-    __shared__ double s_den[kScorePiece][kScoreMaxBorders];
-    __shared__ double s_sc[32];
-    __shared__ int s_bi[32];
+__global__ void __launch_bounds__(kScoreWarps * 32) score_kernel(int level, int32_t F, int32_t B,
+                                                                 const ull* __restrict__ cur,
+                                                                 const int32_t* __restrict__ border_counts,
+                                                                 double l2, int score_fn,
+                                                                 double* __restrict__ grp_score,
+                                                                 int32_t* __restrict__ grp_bin, TreeState* ts) {
+    __shared__ double s_num[kScorePiece][32];
+    __shared__ double s_den[kScorePiece][32];
+    __shared__ double s_sc[kScoreWarps];
+    __shared__ int s_bi[kScoreWarps];
     __shared__ bool s_last;
-    const int f = blockIdx.x;
+    const int g = blockIdx.x, f = blockIdx.y, G = gridDim.x;
     const int nb = border_counts[f];
     const int Q = 1 << level;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int b = g * 32 + lane;
+    const bool in = b < nb;
     const double ig = ts->sc.inv[0], ih = ts->sc.inv[1];
-    // running sums of the border this thread owns (b = threadIdx.x, and
-    // b + kScoreThreads when nb > kScoreThreads; nb <= kScoreMaxBorders)
-    double num[2] = {0.0, 0.0}, den[2] = {1e-100, 1e-100};
-    for (int c0 = 0; c0 < 2 * Q; c0 += kScorePiece) {
-        const int pc = 2 * Q - c0 < kScorePiece ? 2 * Q - c0 : kScorePiece;
-        for (int t = threadIdx.x; t < pc * nb; t += blockDim.x) {
-            const int cc = t / nb, b = t - cc * nb;
-            const int ch = c0 + cc;  // canonical child index: side * Q + q
-            const int side = ch >= Q, q = ch - side * Q;
-            const ull* row = cur + ((size_t)q * F + f) * B * 2;
-            long long pg = (long long)row[2 * b], ph = (long long)row[2 * b + 1];
-            if (side) {
-                pg = (long long)row[2 * (B - 1)] - pg;
-                ph = (long long)row[2 * (B - 1) + 1] - ph;
-            }
-            const double swd = __dmul_rn((double)pg, ig);
-            const double sw = __dmul_rn((double)ph, ih);
-            const double avg = sw > 0.0 ? __ddiv_rn(swd, __dadd_rn(sw, l2)) : 0.0;
-            s_num[cc][b] = __dmul_rn(avg, swd);
-            s_den[cc][b] = __dmul_rn(__dmul_rn(avg, avg), sw);
-        }
-        __syncthreads();
+    double num = 0.0, den = 1e-100;
+    if (g * 32 < nb) {
+        for (int c0 = 0; c0 < 2 * Q; c0 += kScorePiece) {
+            const int pc = 2 * Q - c0 < kScorePiece ? 2 * Q - c0 : kScorePiece;
+            constexpr int kPer = kScorePiece / kScoreWarps;
+            ulonglong2 v[kPer], tot[kPer];
 #pragma unroll
-        for (int k = 0; k < 2; ++k) {
-            const int b = threadIdx.x + k * kScoreThreads;
-            if (b < nb) {
-                for (int cc = 0; cc < pc; ++cc) {
-                    num[k] = __dadd_rn(num[k], s_num[cc][b]);
-                    if (score_fn == 0) den[k] = __dadd_rn(den[k], s_den[cc][b]);
+            for (int k = 0; k < kPer; ++k) {
+                const int cc = warp + k * kScoreWarps;
+                v[k] = make_ulonglong2(0ull, 0ull);
+                tot[k] = make_ulonglong2(0ull, 0ull);
+                if (cc < pc && in) {
+                    const int ch = c0 + cc;  // canonical child index: side * Q + q
+                    const int side = ch >= Q, q = ch - side * Q;
+                    const ulonglong2* row = (const ulonglong2*)(cur + ((size_t)q * F + f) * B * 2);
+                    v[k] = row[b];
+                    if (side) tot[k] = row[B - 1];
                 }
             }
-        }
-        __syncthreads();
-    }
-    double best = -INFINITY;
-    int bbin = 0x7fffffff;
 #pragma unroll
-    for (int k = 0; k < 2; ++k) {
-        const int b = threadIdx.x + k * kScoreThreads;
-        if (b < nb) {
-            double s = score_fn == 0 ? __ddiv_rn(num[k], sqrt(den[k])) : num[k];
-            s = nan_to_neg_inf(s);
-            if (better(s, b, best, bbin)) {
-                best = s;
-                bbin = b;
+            for (int k = 0; k < kPer; ++k) {
+                const int cc = warp + k * kScoreWarps;
+                if (cc < pc && in) {
+                    const int side = c0 + cc >= Q;
+                    long long pg = (long long)v[k].x, ph = (long long)v[k].y;
+                    if (side) {
+                        pg = (long long)tot[k].x - pg;
+                        ph = (long long)tot[k].y - ph;
+                    }
+                    const double swd = __dmul_rn((double)pg, ig);
+                    const double sw = __dmul_rn((double)ph, ih);
+                    const double avg = sw > 0.0 ? __ddiv_rn(swd, __dadd_rn(sw, l2)) : 0.0;
+                    s_num[cc][lane] = __dmul_rn(avg, swd);
+                    s_den[cc][lane] = __dmul_rn(__dmul_rn(avg, avg), sw);
+                }
             }
+            __syncthreads();
+            if (warp == 0 && in) {
+                for (int cc = 0; cc < pc; ++cc) {
+                    num = __dadd_rn(num, s_num[cc][lane]);
+                    if (score_fn == 0) den = __dadd_rn(den, s_den[cc][lane]);
+                }
+            }
+            __syncthreads();
         }
     }
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    if (warp == 0) {
+        double best = -INFINITY;
+        int bbin = 0x7fffffff;
+        if (in) {
+            best = nan_to_neg_inf(score_fn == 0 ? __ddiv_rn(num, sqrt(den)) : num);
+            bbin = b;
+        }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        double os = __shfl_xor_sync(kFull, best, o);
-        int ob = __shfl_xor_sync(kFull, bbin, o);
-        if (better(os, ob, best, bbin)) { best = os; bbin = ob; }
-    }
-    if (lane == 0) { s_sc[warp] = best; s_bi[warp] = bbin; }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        for (int w = 1; w < nw; ++w)
-            if (better(s_sc[w], s_bi[w], best, bbin)) { best = s_sc[w]; bbin = s_bi[w]; }
-        feat_score[f] = best;
-        feat_bin[f] = bbin;
-        __threadfence();
-        unsigned done = atomicAdd(&ts->score_done, 1u);
-        s_last = (done == gridDim.x - 1);
+        for (int o = 16; o > 0; o >>= 1) {
+            double os = __shfl_xor_sync(kFull, best, o);
+            int ob = __shfl_xor_sync(kFull, bbin, o);
+            if (better(os, ob, best, bbin)) { best = os; bbin = ob; }
+        }
+        if (lane == 0) {
+            grp_score[(size_t)f * G + g] = best;
+            grp_bin[(size_t)f * G + g] = bbin;
+            __threadfence();
+            const unsigned done = atomicAdd(&ts->score_done, 1u);
+            s_last = (done == gridDim.x * gridDim.y - 1);
+        }
     }
     __syncthreads();
     if (!s_last) return;
     __threadfence();
+    // (feature, border) order: key f * 256 + border, lowest key wins ties
     double fb = -INFINITY;
-    int fi = 0x7fffffff;
-    for (int ff = threadIdx.x; ff < F; ff += blockDim.x) {
-        double s = ((volatile double*)feat_score)[ff];
-        if (better(s, ff, fb, fi)) { fb = s; fi = ff; }
+    int fk = 0x7fffffff;
+    for (int e = threadIdx.x; e < F * G; e += blockDim.x) {
+        const double sc = ((volatile double*)grp_score)[e];
+        const int bin = ((volatile int32_t*)grp_bin)[e];
+        if (bin == 0x7fffffff) continue;
+        const int key = (e / G) * 256 + bin;
+        if (better(sc, key, fb, fk)) { fb = sc; fk = key; }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
         double os = __shfl_xor_sync(kFull, fb, o);
-        int oi = __shfl_xor_sync(kFull, fi, o);
-        if (better(os, oi, fb, fi)) { fb = os; fi = oi; }
+        int ok = __shfl_xor_sync(kFull, fk, o);
+        if (better(os, ok, fb, fk)) { fb = os; fk = ok; }
     }
-    __syncthreads();
-    if (lane == 0) { s_sc[warp] = fb; s_bi[warp] = fi; }
+    if (lane == 0) { s_sc[warp] = fb; s_bi[warp] = fk; }
     __syncthreads();
     if (threadIdx.x == 0) {
-        for (int w = 1; w < nw; ++w)
-            if (better(s_sc[w], s_bi[w], fb, fi)) { fb = s_sc[w]; fi = s_bi[w]; }
+        for (int w = 1; w < kScoreWarps; ++w)
+            if (better(s_sc[w], s_bi[w], fb, fk)) { fb = s_sc[w]; fk = s_bi[w]; }
         SplitRec rec;
-        if (fi == 0x7fffffff || fb == -INFINITY) {
+        if (fk == 0x7fffffff || fb == -INFINITY) {
             rec.feature = -1;
             rec.bin = -1;
             rec.score = -INFINITY;
             atomicOr(&ts->err, kErrNoCandidate);
         } else {
-            rec.feature = fi;
-            rec.bin = ((volatile int32_t*)feat_bin)[fi];
+            rec.feature = fk >> 8;
+            rec.bin = fk & 255;
             rec.score = fb;
         }
         ts->split[level] = rec;
@@ -1113,10 +1143,11 @@ __global__ void __launch_bounds__(kScoreThreads) score_kernel(int level, int32_t
 }
 
 void launch_score(int level, int32_t F, int32_t B, const ull* cur, const int32_t* border_counts,
-                  double l2, int score_fn, double* feat_score, int32_t* feat_bin, TreeState* ts,
+                  double l2, int score_fn, double* grp_score, int32_t* grp_bin, TreeState* ts,
                   cudaStream_t st) {
-    score_kernel<<<(unsigned)F, kScoreThreads, 0, st>>>(level, F, B, cur, border_counts, l2, score_fn,
-                                              feat_score, feat_bin, ts);
+    const unsigned G = (unsigned)((B - 1 + 31) / 32);  // border groups: borders <= B - 1
+    score_kernel<<<dim3(G > 0 ? G : 1, (unsigned)F), kScoreWarps * 32, 0, st>>>(
+        level, F, B, cur, border_counts, l2, score_fn, grp_score, grp_bin, ts);
 }
 
 // ============================================================================

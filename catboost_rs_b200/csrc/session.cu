@@ -273,8 +273,8 @@ int alloc_session(cbgpu_session* s, const cbgpu_begin_args* a) {
     DA(s->built, s->built_cells);
     DA(s->hist[0], s->hist_cells);
     DA(s->hist[1], s->hist_cells);
-    DA(s->feat_score, s->F);
-    DA(s->feat_bin, s->F);
+    DA(s->feat_score, (size_t)s->F * 8);  // per (feature, 32-border group) winners
+    DA(s->feat_bin, (size_t)s->F * 8);
     DA(s->leaf_sums, 2 * L);
     DA(s->leaf_raw, L);
     DA(s->leaf_lrv, L);
