@@ -113,6 +113,7 @@ enum : uint32_t {
     kErrBinRange = 1u << 1,      // a bin index >= n_bins was seen
     kErrOverflow = 1u << 2,      // fixed-point range exceeded
     kErrLeafRange = 1u << 3,     // leaf id out of range
+    kErrChunkCap = 1u << 4,      // the histogram work list exceeded its buffer
 };
 
 }  // namespace cbgpu

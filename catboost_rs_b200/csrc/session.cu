@@ -124,6 +124,7 @@ struct cbgpu_session {
 
     cudaStream_t st = nullptr;
     ncclComm_t comm = nullptr;
+    bool broken = false;  // a multi-rank grow failed: peers may be waiting in a collective
 
     // device data
     uint8_t* bins_rm = nullptr;   // [n][F_pad]
@@ -146,6 +147,7 @@ struct cbgpu_session {
     uint32_t* flags = nullptr;    // split outcome bit per row (natural order)
     uint8_t* small_side = nullptr;
     HistChunk* chunks = nullptr;
+    size_t chunk_cap = 0;
     uint32_t* n_chunks = nullptr;
     ull* built = nullptr;
     ull* hist[2] = {nullptr, nullptr};
@@ -265,9 +267,10 @@ int alloc_session(cbgpu_session* s, const cbgpu_begin_args* a) {
     DA(s->child_cnt, 1 << 17);
     DA(s->flags, 2 * ((n + 31) / 32 + 1));  // natural-order outcome bits, then position-order words
     DA(s->small_side, 1 << 16);
-    const size_t max_chunks = (size_t)(n / kChunkRows) + (L / 2) + 2;
-    DA(s->chunks, max_chunks);
-    DA(s->n_chunks, 1);
+    // chunks are as small as kChunkRows / 4 rows, plus one partial chunk per segment
+    s->chunk_cap = (size_t)(n / (kChunkRows / 4)) + (L / 2) + 2;
+    DA(s->chunks, s->chunk_cap);
+    DA(s->n_chunks, 2);  // chunk count, histogram work counter
     s->built_cells = (size_t)(L / 2 > 0 ? L / 2 : 1) * s->F * s->B * 2;
     s->hist_cells = (size_t)(L / 2 > 0 ? L / 2 : 1) * s->F * s->B * 2;
     DA(s->built, s->built_cells);
@@ -307,6 +310,13 @@ int alloc_session(cbgpu_session* s, const cbgpu_begin_args* a) {
 void free_session(cbgpu_session* s) {
     if (!s) return;
     cudaSetDevice(s->device);
+    // After a failed multi-rank step this rank's queued collectives may never
+    // complete (the peers went their own way), so the communicator is aborted
+    // before the stream is drained instead of destroyed after it.
+    if (s->broken && s->comm) {
+        ncclCommAbort(s->comm);
+        s->comm = nullptr;
+    }
     if (s->st) cudaStreamSynchronize(s->st);
     void* ptrs[] = {s->bins_rm, s->bins_fm, s->d_border_counts, s->target, s->weight, s->approx,
                     s->wd1, s->qstats, s->sw32, s->sw64, s->mvs_thr, s->leaf, s->perm[0], s->perm[1],
@@ -516,12 +526,13 @@ int grow(cbgpu_session* s, const double* approx_h, const double* target_h, int64
         const size_t built_slots = l == 0 ? 1 : (size_t)1 << (l - 1);
         CU(cudaMemsetAsync(s->built, 0, sizeof(ull) * built_slots * row_cells, st));
         const uint32_t max_chunks =
-            (uint32_t)(s->n / kChunkRows + (l == 0 ? 1 : (1u << (l - 1))) + 1);
+            (uint32_t)(s->n / (kChunkRows / 4) + (l == 0 ? 1 : (1u << (l - 1))) + 1);
         launch_make_chunks(l, s->sg.seg_off, s->sg.seg_cnt, s->sg.mem_start, s->sg.mem_leaf,
-                           l ? s->small_side : nullptr, s->n, s->chunks, s->n_chunks, s->ts, st);
+                           l ? s->small_side : nullptr, s->n, (uint32_t)hist_tiles(s->F, s->B), s->chunks,
+                           (uint32_t)s->chunk_cap, s->n_chunks, s->ts, st);
         rec(e);
         launch_hist(s->bins_rm, s->F_pad, s->F, s->B, s->qstats, l == 0 ? nullptr : s->perm[pp], s->chunks,
-                    s->n_chunks, max_chunks, s->built, st);
+                    s->n_chunks, max_chunks, s->built, (int64_t)s->B * 2, (int64_t)s->F * s->B * 2, st);
         rec(e + 1);
         launches += 2;
         {
@@ -734,8 +745,10 @@ int cbgpu_grow_tree(cbgpu_session* s, const double* approx, const double* target
                     const double* sample, int64_t sample_len, int32_t* split_feature, int32_t* split_bin,
                     int32_t* n_splits, double* leaf_values, void* leaf_of, int32_t leaf_of_bytes) {
     if (!s) return fail(CBGPU_ERR_INVALID, "null session");
-    return grow(s, approx, target, n, sample, sample_len, split_feature, split_bin, n_splits,
-                leaf_values, leaf_of, leaf_of_bytes);
+    const int rc = grow(s, approx, target, n, sample, sample_len, split_feature, split_bin, n_splits,
+                        leaf_values, leaf_of, leaf_of_bytes);
+    if (rc != CBGPU_OK && s->world > 1) s->broken = true;
+    return rc;
 }
 
 int cbgpu_end(cbgpu_session* s) {
@@ -916,16 +929,18 @@ int cbgpu_histogram(const uint8_t* bins_rm_h, int64_t n, int32_t F, int32_t B, c
     DA(d_qs, qs.size());
     DA(d_perm, std::max<size_t>(perm.size(), 1));
     DA(d_ch, std::max<size_t>(chunks.size(), 1));
-    DA(d_nch, 1);
+    DA(d_nch, 2);
     DA(d_out, cells);
-    uint32_t nch = (uint32_t)chunks.size();
+    const uint32_t nch_ctr[2] = {(uint32_t)chunks.size(), 0u};  // chunk count, work counter
+    const uint32_t nch = nch_ctr[0];
     CU(cudaMemcpy(d_rm, rm.data(), rm.size(), cudaMemcpyHostToDevice));
     CU(cudaMemcpy(d_qs, qs.data(), sizeof(uint4) * qs.size(), cudaMemcpyHostToDevice));
     if (!perm.empty()) CU(cudaMemcpy(d_perm, perm.data(), sizeof(uint32_t) * perm.size(), cudaMemcpyHostToDevice));
     if (!chunks.empty()) CU(cudaMemcpy(d_ch, chunks.data(), sizeof(HistChunk) * chunks.size(), cudaMemcpyHostToDevice));
-    CU(cudaMemcpy(d_nch, &nch, sizeof(uint32_t), cudaMemcpyHostToDevice));
+    CU(cudaMemcpy(d_nch, nch_ctr, sizeof(nch_ctr), cudaMemcpyHostToDevice));
     CU(cudaMemset(d_out, 0, sizeof(ull) * cells));
-    launch_hist(d_rm, F_pad, F, B, d_qs, d_perm, d_ch, d_nch, std::max<uint32_t>(nch, 1), d_out, 0);
+    launch_hist(d_rm, F_pad, F, B, d_qs, d_perm, d_ch, d_nch, std::max<uint32_t>(nch, 1), d_out, (int64_t)B * 2,
+                (int64_t)F * B * 2, 0);
     CU(cudaGetLastError());
     std::vector<ull> hout(cells);
     CU(cudaMemcpy(hout.data(), d_out, sizeof(ull) * cells, cudaMemcpyDeviceToHost));
