@@ -742,34 +742,26 @@ template <bool kGather, int kFplFull, int kWarps, int kStages>
 __global__ void __launch_bounds__(kWarps * 32, 1) hist_kernel(
     const uint8_t* __restrict__ bins_rm, int32_t F_pad, int32_t F, int32_t B,
     const uint4* __restrict__ qstats, const uint32_t* __restrict__ perm,
-    const HistChunk* __restrict__ chunks, uint32_t* __restrict__ n_chunks,
+    const HistChunk* __restrict__ chunks, const uint32_t* __restrict__ n_chunks,
     ull* __restrict__ built, int64_t feat_stride, int64_t slot_stride) {
     extern __shared__ __align__(16) uint32_t hs[];  // table [B][4][32*fpl] then the staging ring
-    __shared__ uint32_t s_item[2];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     constexpr int kSlice = 32 * kFplFull;  // staged bytes per row
     const size_t table_words = (size_t)B * 128 * kFplFull;
     uint8_t* sbins = (uint8_t*)(hs + table_words) + (size_t)warp * kStages * 32 * kSlice;
     uint4* sstat = (uint4*)((uint8_t*)(hs + table_words) + (size_t)kWarps * kStages * 32 * kSlice) +
                    (size_t)warp * kStages * 32;
-    const uint32_t T = (uint32_t)hist_n_tiles(F, kFplFull);
-    const uint32_t n_items = n_chunks[0] * T;
-    // persistent blocks take (chunk, tile) items in tile-fastest order from the
-    // counter n_chunks[1], so the blocks running together read the same rows;
-    // the next item is claimed while the current one is processed
-    if (threadIdx.x == 0) s_item[0] = atomicAdd(n_chunks + 1, 1u);
-    __syncthreads();
-    for (int it = 0;; it ^= 1) {
-    const uint32_t item = s_item[it];
-    if (item >= n_items) break;
-    uint32_t next = 0;
-    if (threadIdx.x == 0) next = atomicAdd(n_chunks + 1, 1u);
-    const HistChunk ck = chunks[item / T];
-    const TileInfo ti = hist_tile(F, kFplFull, (int)(item % T));
+    // grid: x = feature tile (fastest, so the tiles of a chunk run together and
+    // share the chunk's rows in L2), y = chunk (striding when there are more
+    // chunks than grid rows)
+    const TileInfo ti = hist_tile(F, kFplFull, blockIdx.x);
     // 16-byte pieces of the row slice this tile needs
     const int pieces = ti.kind == 2 ? 4 : (ti.kind == 1 ? 2 : (ti.nf > 16 ? 2 : 1));
     const int narrow_w = ti.nf > 16 ? 32 : ti.nf > 8 ? 16 : ti.nf > 4 ? 8 : ti.nf > 2 ? 4 : ti.nf > 1 ? 2 : 1;
     const uint8_t* tile_base = bins_rm + ti.f0;
+    const uint32_t nch = n_chunks[0];
+    for (uint32_t c = blockIdx.y; c < nch; c += gridDim.y) {
+    const HistChunk ck = chunks[c];
     for (size_t k = threadIdx.x; k < table_words / 4; k += blockDim.x) ((uint4*)hs)[k] = make_uint4(0u, 0u, 0u, 0u);
     __syncthreads();
 
@@ -846,8 +838,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1) hist_kernel(
     else if (narrow_w == 4) hist_flush<1, 4>(hs, B, ti.nf, out, feat_stride);
     else if (narrow_w == 2) hist_flush<1, 2>(hs, B, ti.nf, out, feat_stride);
     else hist_flush<1, 1>(hs, B, ti.nf, out, feat_stride);
-    if (threadIdx.x == 0) s_item[it ^ 1] = next;
-    __syncthreads();  // the table is zeroed again for the next item
+    __syncthreads();  // the table is zeroed again for the next chunk
     }
 }
 
@@ -871,73 +862,49 @@ static HistShape hist_shape(int32_t B) {
 size_t hist_smem_bytes(int32_t B) { return hist_shape_bytes(B, hist_shape(B)); }
 
 template <bool kGather, int kFpl, int kWarps, int kStages>
-static void launch_hist_variant(uint32_t max_items, cudaStream_t st, const uint8_t* bins_rm, int32_t F_pad,
-                                int32_t F, int32_t B, const uint4* qstats, const uint32_t* perm,
-                                const HistChunk* chunks, uint32_t* n_chunks, ull* built, int64_t feat_stride,
-                                int64_t slot_stride) {
+static void launch_hist_variant(unsigned gy, cudaStream_t st, const uint8_t* bins_rm, int32_t F_pad, int32_t F,
+                                int32_t B, const uint4* qstats, const uint32_t* perm, const HistChunk* chunks,
+                                const uint32_t* n_chunks, ull* built, int64_t feat_stride, int64_t slot_stride) {
     static int attr_device = -1, attr_bins = -1;
-    static int resident = 1;  // blocks per SM at this variant's shared memory
-    static int sms = 148;
     int dev = 0;
     cudaGetDevice(&dev);
     if (attr_device != dev || attr_bins != B) {
         cudaFuncSetAttribute(hist_kernel<kGather, kFpl, kWarps, kStages>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)hist_smem_bytes(B));
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        int r = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&r, hist_kernel<kGather, kFpl, kWarps, kStages>,
-                                                          kWarps * 32, hist_smem_bytes(B)) != cudaSuccess || r < 1)
-            r = 1;
-        resident = r;
         attr_device = dev;
         attr_bins = B;
     }
-    const uint32_t cap = (uint32_t)(sms * resident);
-    const uint32_t blocks = max_items < cap ? max_items : cap;
-    hist_kernel<kGather, kFpl, kWarps, kStages><<<blocks, kWarps * 32, hist_smem_bytes(B), st>>>(
+    const dim3 grid((unsigned)hist_n_tiles(F, kFpl), gy);
+    hist_kernel<kGather, kFpl, kWarps, kStages><<<grid, kWarps * 32, hist_smem_bytes(B), st>>>(
         bins_rm, F_pad, F, B, qstats, perm, chunks, n_chunks, built, feat_stride, slot_stride);
 }
 
 int hist_tiles(int32_t F, int32_t B) { return hist_n_tiles(F, hist_shape(B).fpl); }
 
 void launch_hist(const uint8_t* bins_rm, int32_t F_pad, int32_t F, int32_t B, const uint4* qstats,
-                 const uint32_t* perm, const HistChunk* chunks, uint32_t* n_chunks, uint32_t max_chunks,
+                 const uint32_t* perm, const HistChunk* chunks, const uint32_t* n_chunks, uint32_t max_chunks,
                  ull* built, int64_t feat_stride, int64_t slot_stride, cudaStream_t st) {
     if (max_chunks == 0) return;
+    const unsigned gy = max_chunks < 65535u ? max_chunks : 65535u;
     const bool two = hist_shape(B).fpl == 2;
-    const uint32_t max_items = max_chunks * (uint32_t)hist_tiles(F, B);
     if (perm) {
-        if (two) launch_hist_variant<true, 2, 16, 2>(max_items, st, bins_rm, F_pad, F, B, qstats, perm, chunks, n_chunks, built, feat_stride, slot_stride);
-        else launch_hist_variant<true, 1, 8, 3>(max_items, st, bins_rm, F_pad, F, B, qstats, perm, chunks, n_chunks, built, feat_stride, slot_stride);
+        if (two) launch_hist_variant<true, 2, 16, 2>(gy, st, bins_rm, F_pad, F, B, qstats, perm, chunks, n_chunks, built, feat_stride, slot_stride);
+        else launch_hist_variant<true, 1, 8, 3>(gy, st, bins_rm, F_pad, F, B, qstats, perm, chunks, n_chunks, built, feat_stride, slot_stride);
     } else {
-        if (two) launch_hist_variant<false, 2, 16, 2>(max_items, st, bins_rm, F_pad, F, B, qstats, perm, chunks, n_chunks, built, feat_stride, slot_stride);
-        else launch_hist_variant<false, 1, 8, 3>(max_items, st, bins_rm, F_pad, F, B, qstats, perm, chunks, n_chunks, built, feat_stride, slot_stride);
+        if (two) launch_hist_variant<false, 2, 16, 2>(gy, st, bins_rm, F_pad, F, B, qstats, perm, chunks, n_chunks, built, feat_stride, slot_stride);
+        else launch_hist_variant<false, 1, 8, 3>(gy, st, bins_rm, F_pad, F, B, qstats, perm, chunks, n_chunks, built, feat_stride, slot_stride);
     }
-}
-
-// Work list for the level: level 0 = all rows (identity order) in one slot;
-// level l >= 1 = for each parent p the smaller child's leaf-sorted segment
-// into slot p, cut into kChunkRows pieces.  Level 0 also initialises the
-// segment tables to the single all-rows segment.
-// Rows per work item: the largest of kChunkRows, /2, /4 that still gives the
-// persistent histogram blocks about kHistMinItems (chunk, tile) items, so a
-// level with few rows (a deep level, or a shard of a multi-GPU fit) does not
-// leave SMs idle; kChunkRows also bounds the 32-bit partial sums.
-__device__ __forceinline__ uint32_t chunk_rows_for(uint64_t rows, uint32_t tiles) {
-    uint32_t cr = kChunkRows;
-    while (cr > kChunkRows / 4 && rows / cr * tiles < (uint64_t)kHistMinItems) cr >>= 1;
-    return cr;
 }
 
 __global__ void make_chunks_kernel(int level, uint32_t* __restrict__ seg_off,
                                    uint32_t* __restrict__ seg_cnt, uint32_t* __restrict__ mem_start,
                                    uint32_t* __restrict__ mem_leaf,
-                                   const uint8_t* __restrict__ small_side, int64_t n0, uint32_t tiles,
+                                   const uint8_t* __restrict__ small_side, int64_t n0,
                                    HistChunk* __restrict__ chunks, uint32_t cap, uint32_t* __restrict__ n_chunks,
                                    TreeState* ts) {
     __shared__ uint32_t s_scan[40];
     if (level == 0) {
-        const uint32_t cr = chunk_rows_for((uint64_t)n0, tiles);
+        const uint32_t cr = kChunkRows;
         uint32_t nch = (uint32_t)((n0 + cr - 1) / cr);
         if (nch > cap) {  // cannot happen with the session's sizing; never write past the buffer
             if (threadIdx.x == 0) atomicOr(&ts->err, kErrChunkCap);
@@ -950,7 +917,6 @@ __global__ void make_chunks_kernel(int level, uint32_t* __restrict__ seg_off,
         }
         if (threadIdx.x == 0) {
             n_chunks[0] = nch;
-            n_chunks[1] = 0u;  // work counter of the histogram launch
             seg_off[0] = 0u;
             seg_cnt[0] = (uint32_t)n0;
             mem_start[0] = 0u;
@@ -966,7 +932,7 @@ __global__ void make_chunks_kernel(int level, uint32_t* __restrict__ seg_off,
     for (uint32_t p = p0; p < p0 + per && p < half; ++p) rows += seg_cnt[small_side[p] ? p + half : p];
     uint32_t rows_tot;
     (void)block_excl_scan<uint32_t>(rows, s_scan, &rows_tot);
-    const uint32_t cr = chunk_rows_for(rows_tot, tiles);
+    const uint32_t cr = kChunkRows;
     uint32_t cnt = 0;
     for (uint32_t p = p0; p < p0 + per && p < half; ++p) cnt += (seg_cnt[small_side[p] ? p + half : p] + cr - 1) / cr;
     uint32_t tot;
@@ -985,16 +951,15 @@ __global__ void make_chunks_kernel(int level, uint32_t* __restrict__ seg_off,
             tot = cap;
         }
         n_chunks[0] = tot;
-        n_chunks[1] = 0u;
         ts->hist_rows[level] = rows_tot;
     }
 }
 
 void launch_make_chunks(int level, uint32_t* seg_off, uint32_t* seg_cnt, uint32_t* mem_start,
-                        uint32_t* mem_leaf, const uint8_t* small_side, int64_t n_level0, uint32_t tiles,
+                        uint32_t* mem_leaf, const uint8_t* small_side, int64_t n_level0,
                         HistChunk* chunks, uint32_t cap, uint32_t* n_chunks, TreeState* ts, cudaStream_t st) {
     make_chunks_kernel<<<1, 1024, 0, st>>>(level, seg_off, seg_cnt, mem_start, mem_leaf, small_side,
-                                           n_level0, tiles, chunks, cap, n_chunks, ts);
+                                           n_level0, chunks, cap, n_chunks, ts);
 }
 
 // ============================================================================

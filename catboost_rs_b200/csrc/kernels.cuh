@@ -47,7 +47,6 @@ struct TreeState {
 
 constexpr int kTile = 32;          // features per histogram tile (one per lane)
 constexpr int kHistSmemMax = 227 * 1024;  // dynamic shared memory opt-in limit per block
-constexpr int kHistMinItems = 148 * 6;    // (chunk, tile) items a level aims for (rows permitting)
 constexpr int kChunkRows = 16384;  // rows per histogram work item
 // Score-channel fixed point: |row value| <= 2^kPackBits, split at bit kPackSplit
 // into (lo, hi) u32 parts whose sums over kChunkRows rows stay below 2^31.
@@ -106,17 +105,16 @@ void launch_apply(int64_t n, double* approx, const uint16_t* leaf, const double*
 
 // ---- per level ---------------------------------------------------------------
 void launch_zero(void* p, size_t bytes, cudaStream_t st);
-int hist_tiles(int32_t F, int32_t B);  // (chunk, tile) items per chunk
-// n_chunks: {chunk count, work counter (zero before the launch)}; max_chunks
-// bounds the chunk count.  Cell (slot, f, bin, c) of the output is
-// built[slot * slot_stride + f * feat_stride + bin * 2 + c].
+int hist_tiles(int32_t F, int32_t B);  // feature tiles (grid x) of the histogram launch
+// n_chunks: device chunk count; max_chunks bounds it.  Cell (slot, f, bin, c)
+// of the output is built[slot * slot_stride + f * feat_stride + bin * 2 + c].
 void launch_hist(const uint8_t* bins_rm, int32_t F_pad, int32_t F, int32_t B, const uint4* qstats,
-                 const uint32_t* perm, const HistChunk* chunks, uint32_t* n_chunks, uint32_t max_chunks,
+                 const uint32_t* perm, const HistChunk* chunks, const uint32_t* n_chunks, uint32_t max_chunks,
                  ull* built, int64_t feat_stride, int64_t slot_stride, cudaStream_t st);
 // level 0 also initialises the segment tables to the single all-rows segment.
-// cap = entries of `chunks`: at most n / (kChunkRows / 4) + 2^(level-1) + 1 are written.
+// cap = entries of `chunks`: at most n / kChunkRows + 2^(level-1) + 1 are written.
 void launch_make_chunks(int level, uint32_t* seg_off, uint32_t* seg_cnt, uint32_t* mem_start,
-                        uint32_t* mem_leaf, const uint8_t* small_side, int64_t n_level0, uint32_t tiles,
+                        uint32_t* mem_leaf, const uint8_t* small_side, int64_t n_level0,
                         HistChunk* chunks, uint32_t cap, uint32_t* n_chunks, TreeState* ts, cudaStream_t st);
 void launch_derive_prefix(int level, int32_t F, int32_t B, const ull* built, const ull* prev,
                           ull* cur, const uint8_t* small_side, cudaStream_t st);

@@ -53,8 +53,7 @@ namespace {
 
 int na_fail(int code, const std::string& msg) { return cbgpu::record_error(code, msg.c_str()); }
 
-// Zeroes what must start at zero (the int64 accumulators, the maxima and the
-// histogram's work counter) and
+// Zeroes what must start at zero (the int64 accumulators and the maxima) and
 // writes the all-rows work list: the array keeps the previous call's contents.
 __global__ void na_init_kernel(int64_t n, int64_t cells) {
     ull* acc = (ull*)(g_na_scratch + kOffAcc);
@@ -69,8 +68,7 @@ __global__ void na_init_kernel(int64_t n, int64_t cells) {
             ch[k] = HistChunk{0u, st, (uint32_t)(n - st < kChunkRows ? n - st : kChunkRows), 0u};
         }
         if (threadIdx.x == 0) {
-            ((uint32_t*)(g_na_scratch + kOffNChunks))[0] = nch;
-            ((uint32_t*)(g_na_scratch + kOffNChunks))[1] = 0u;  // histogram work counter
+            *(uint32_t*)(g_na_scratch + kOffNChunks) = nch;
             ull* mx = (ull*)(g_na_scratch + kOffMax);
             mx[0] = 0ull;
             mx[1] = 0ull;
@@ -185,7 +183,7 @@ int cbgpu_histogram_noalloc(const uint8_t* d_bins_row_major, int64_t n, int32_t 
         na_max_kernel<<<grid_for(n), 256, 0, st>>>(n, d_g, d_h);
         na_pack_kernel<<<grid_for(n), 256, 0, st>>>(n, d_g, d_h);
         launch_hist(d_bins_row_major, row_stride, n_features, n_bins, (const uint4*)(base + kOffQstats),
-                    nullptr, (const HistChunk*)(base + kOffChunks), (uint32_t*)(base + kOffNChunks),
+                    nullptr, (const HistChunk*)(base + kOffChunks), (const uint32_t*)(base + kOffNChunks),
                     (uint32_t)((n + kChunkRows - 1) / kChunkRows), (ull*)(base + kOffAcc), (int64_t)n_bins * 2,
                     (int64_t)n_features * n_bins * 2, st);
     }

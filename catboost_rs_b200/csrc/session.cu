@@ -267,10 +267,10 @@ int alloc_session(cbgpu_session* s, const cbgpu_begin_args* a) {
     DA(s->child_cnt, 1 << 17);
     DA(s->flags, 2 * ((n + 31) / 32 + 1));  // natural-order outcome bits, then position-order words
     DA(s->small_side, 1 << 16);
-    // chunks are as small as kChunkRows / 4 rows, plus one partial chunk per segment
-    s->chunk_cap = (size_t)(n / (kChunkRows / 4)) + (L / 2) + 2;
+    // full chunks plus one partial chunk per segment
+    s->chunk_cap = (size_t)(n / kChunkRows) + (L / 2) + 2;
     DA(s->chunks, s->chunk_cap);
-    DA(s->n_chunks, 2);  // chunk count, histogram work counter
+    DA(s->n_chunks, 1);
     s->built_cells = (size_t)(L / 2 > 0 ? L / 2 : 1) * s->F * s->B * 2;
     s->hist_cells = (size_t)(L / 2 > 0 ? L / 2 : 1) * s->F * s->B * 2;
     DA(s->built, s->built_cells);
@@ -526,10 +526,10 @@ int grow(cbgpu_session* s, const double* approx_h, const double* target_h, int64
         const size_t built_slots = l == 0 ? 1 : (size_t)1 << (l - 1);
         CU(cudaMemsetAsync(s->built, 0, sizeof(ull) * built_slots * row_cells, st));
         const uint32_t max_chunks =
-            (uint32_t)(s->n / (kChunkRows / 4) + (l == 0 ? 1 : (1u << (l - 1))) + 1);
+            (uint32_t)(s->n / kChunkRows + (l == 0 ? 1 : (1u << (l - 1))) + 1);
         launch_make_chunks(l, s->sg.seg_off, s->sg.seg_cnt, s->sg.mem_start, s->sg.mem_leaf,
-                           l ? s->small_side : nullptr, s->n, (uint32_t)hist_tiles(s->F, s->B), s->chunks,
-                           (uint32_t)s->chunk_cap, s->n_chunks, s->ts, st);
+                           l ? s->small_side : nullptr, s->n, s->chunks, (uint32_t)s->chunk_cap, s->n_chunks,
+                           s->ts, st);
         rec(e);
         launch_hist(s->bins_rm, s->F_pad, s->F, s->B, s->qstats, l == 0 ? nullptr : s->perm[pp], s->chunks,
                     s->n_chunks, max_chunks, s->built, (int64_t)s->B * 2, (int64_t)s->F * s->B * 2, st);
@@ -929,15 +929,14 @@ int cbgpu_histogram(const uint8_t* bins_rm_h, int64_t n, int32_t F, int32_t B, c
     DA(d_qs, qs.size());
     DA(d_perm, std::max<size_t>(perm.size(), 1));
     DA(d_ch, std::max<size_t>(chunks.size(), 1));
-    DA(d_nch, 2);
+    DA(d_nch, 1);
     DA(d_out, cells);
-    const uint32_t nch_ctr[2] = {(uint32_t)chunks.size(), 0u};  // chunk count, work counter
-    const uint32_t nch = nch_ctr[0];
+    const uint32_t nch = (uint32_t)chunks.size();
     CU(cudaMemcpy(d_rm, rm.data(), rm.size(), cudaMemcpyHostToDevice));
     CU(cudaMemcpy(d_qs, qs.data(), sizeof(uint4) * qs.size(), cudaMemcpyHostToDevice));
     if (!perm.empty()) CU(cudaMemcpy(d_perm, perm.data(), sizeof(uint32_t) * perm.size(), cudaMemcpyHostToDevice));
     if (!chunks.empty()) CU(cudaMemcpy(d_ch, chunks.data(), sizeof(HistChunk) * chunks.size(), cudaMemcpyHostToDevice));
-    CU(cudaMemcpy(d_nch, nch_ctr, sizeof(nch_ctr), cudaMemcpyHostToDevice));
+    CU(cudaMemcpy(d_nch, &nch, sizeof(uint32_t), cudaMemcpyHostToDevice));
     CU(cudaMemset(d_out, 0, sizeof(ull) * cells));
     launch_hist(d_rm, F_pad, F, B, d_qs, d_perm, d_ch, d_nch, std::max<uint32_t>(nch, 1), d_out, (int64_t)B * 2,
                 (int64_t)F * B * 2, 0);
