@@ -967,17 +967,20 @@ void launch_make_chunks(int level, uint32_t* seg_off, uint32_t* seg_cnt, uint32_
 // Level 0: prefix(built[0]).  Level l: parent p = q mod 2^(l-1); the built child
 // of p is copied, the other is prev[p] - prefix(built[p]) (exact integers; the
 // subtraction trick of tree.rs:1075-1131 applied to prefix sums, which are linear).
-// One warp per (leaf, feature) row.
+// One warp per (leaf, feature) row.  All three arrays are feature-major over
+// this rank's feature slice of Fs features: built[f][slot][B][2] (slots =
+// 2^(level-1) parents, 1 at level 0), prev[f][Q/2][B][2], cur[f][Q][B][2].
 // ============================================================================
-__global__ void derive_prefix_kernel(int level, int32_t F, int32_t B, const ull* __restrict__ built,
+__global__ void derive_prefix_kernel(int level, int32_t Fs, int32_t B, const ull* __restrict__ built,
                                      const ull* __restrict__ prev, ull* __restrict__ cur,
                                      const uint8_t* __restrict__ small_side) {
     const int lane = threadIdx.x & 31;
     const int64_t row = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
     const int64_t Q = 1ll << level;
-    if (row >= Q * F) return;
-    const int64_t q = row / F;
-    const int f = (int)(row % F);
+    const int64_t slots = level > 0 ? Q >> 1 : 1;
+    if (row >= Q * Fs) return;
+    const int f = (int)(row / Q);
+    const int64_t q = row % Q;
     int64_t p = 0;
     bool is_built = true;
     if (level > 0) {
@@ -985,9 +988,9 @@ __global__ void derive_prefix_kernel(int level, int32_t F, int32_t B, const ull*
         p = q & (half - 1);
         is_built = ((q >> (level - 1)) & 1) == (int64_t)small_side[p];
     }
-    const ulonglong2* src = (const ulonglong2*)(built + ((size_t)p * F + f) * B * 2);
-    const ulonglong2* par = (level > 0) ? (const ulonglong2*)(prev + ((size_t)p * F + f) * B * 2) : nullptr;
-    ulonglong2* dst = (ulonglong2*)(cur + ((size_t)q * F + f) * B * 2);
+    const ulonglong2* src = (const ulonglong2*)(built + ((size_t)f * slots + p) * B * 2);
+    const ulonglong2* par = (level > 0) ? (const ulonglong2*)(prev + ((size_t)f * slots + p) * B * 2) : nullptr;
+    ulonglong2* dst = (ulonglong2*)(cur + ((size_t)f * Q + q) * B * 2);
     // bins b = 32k + lane: coalesced 16-byte (g, h) pairs, prefix carried across rounds
     long long cg = 0, ch = 0;
     for (int b0 = 0; b0 < B; b0 += 32) {
@@ -1009,11 +1012,12 @@ __global__ void derive_prefix_kernel(int level, int32_t F, int32_t B, const ull*
     }
 }
 
-void launch_derive_prefix(int level, int32_t F, int32_t B, const ull* built, const ull* prev,
+void launch_derive_prefix(int level, int32_t Fs, int32_t B, const ull* built, const ull* prev,
                           ull* cur, const uint8_t* small_side, cudaStream_t st) {
-    int64_t rows = (1ll << level) * F;
+    int64_t rows = (1ll << level) * Fs;
     int64_t blocks = (rows * 32 + 255) / 256;
-    derive_prefix_kernel<<<(unsigned)blocks, 256, 0, st>>>(level, F, B, built, prev, cur, small_side);
+    if (blocks < 1) return;
+    derive_prefix_kernel<<<(unsigned)blocks, 256, 0, st>>>(level, Fs, B, built, prev, cur, small_side);
 }
 
 // ============================================================================
@@ -1030,19 +1034,21 @@ void launch_derive_prefix(int level, int32_t F, int32_t B, const ull* built, con
 constexpr int kScoreWarps = 8;
 constexpr int kScorePiece = 64;  // children per piece, kScorePiece / kScoreWarps per warp
 
-__global__ void __launch_bounds__(kScoreWarps * 32) score_kernel(int level, int32_t F, int32_t B,
-                                                                 const ull* __restrict__ cur,
+__global__ void __launch_bounds__(kScoreWarps * 32) score_kernel(int level, int32_t Fs, int32_t f0, int32_t F,
+                                                                 int32_t B, const ull* __restrict__ cur,
                                                                  const int32_t* __restrict__ border_counts,
                                                                  double l2, int score_fn,
                                                                  double* __restrict__ grp_score,
-                                                                 int32_t* __restrict__ grp_bin, TreeState* ts) {
+                                                                 int32_t* __restrict__ grp_bin, TreeState* ts,
+                                                                 ull* __restrict__ rank_best) {
     __shared__ double s_num[kScorePiece][32];
     __shared__ double s_den[kScorePiece][32];
     __shared__ double s_sc[kScoreWarps];
     __shared__ int s_bi[kScoreWarps];
     __shared__ bool s_last;
-    const int g = blockIdx.x, f = blockIdx.y, G = gridDim.x;
-    const int nb = border_counts[f];
+    const int g = blockIdx.x, fl = blockIdx.y, G = gridDim.x;
+    const int f = f0 + fl;  // global feature
+    const int nb = f < F ? border_counts[f] : 0;
     const int Q = 1 << level;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int b = g * 32 + lane;
@@ -1062,7 +1068,7 @@ __global__ void __launch_bounds__(kScoreWarps * 32) score_kernel(int level, int3
                 if (cc < pc && in) {
                     const int ch = c0 + cc;  // canonical child index: side * Q + q
                     const int side = ch >= Q, q = ch - side * Q;
-                    const ulonglong2* row = (const ulonglong2*)(cur + ((size_t)q * F + f) * B * 2);
+                    const ulonglong2* row = (const ulonglong2*)(cur + ((size_t)fl * Q + q) * B * 2);
                     v[k] = row[b];
                     if (side) tot[k] = row[B - 1];
                 }
@@ -1108,8 +1114,8 @@ __global__ void __launch_bounds__(kScoreWarps * 32) score_kernel(int level, int3
             if (better(os, ob, best, bbin)) { best = os; bbin = ob; }
         }
         if (lane == 0) {
-            grp_score[(size_t)f * G + g] = best;
-            grp_bin[(size_t)f * G + g] = bbin;
+            grp_score[(size_t)fl * G + g] = best;
+            grp_bin[(size_t)fl * G + g] = bbin;
             __threadfence();
             const unsigned done = atomicAdd(&ts->score_done, 1u);
             s_last = (done == gridDim.x * gridDim.y - 1);
@@ -1121,11 +1127,11 @@ __global__ void __launch_bounds__(kScoreWarps * 32) score_kernel(int level, int3
     // (feature, border) order: key f * 256 + border, lowest key wins ties
     double fb = -INFINITY;
     int fk = 0x7fffffff;
-    for (int e = threadIdx.x; e < F * G; e += blockDim.x) {
+    for (int e = threadIdx.x; e < Fs * G; e += blockDim.x) {
         const double sc = ((volatile double*)grp_score)[e];
         const int bin = ((volatile int32_t*)grp_bin)[e];
         if (bin == 0x7fffffff) continue;
-        const int key = (e / G) * 256 + bin;
+        const int key = (f0 + e / G) * 256 + bin;
         if (better(sc, key, fb, fk)) { fb = sc; fk = key; }
     }
 #pragma unroll
@@ -1139,6 +1145,31 @@ __global__ void __launch_bounds__(kScoreWarps * 32) score_kernel(int level, int3
     if (threadIdx.x == 0) {
         for (int w = 1; w < kScoreWarps; ++w)
             if (better(s_sc[w], s_bi[w], fb, fk)) { fb = s_sc[w]; fk = s_bi[w]; }
+        ts->score_done = 0;
+        if (rank_best) {  // this rank's feature slice: (score bits, key) for the all-gather
+            rank_best[0] = (ull)__double_as_longlong(fb);
+            rank_best[1] = (ull)(uint32_t)fk;
+            s_bi[0] = fk;
+        }
+    }
+    if (rank_best) {
+        // ... followed by the slice winner's per-leaf (false, true) weight
+        // channel sums, from which every rank picks the smaller child to build
+        __syncthreads();
+        const int k = s_bi[0];
+        for (int q = threadIdx.x; q < Q; q += blockDim.x) {
+            ull fm = 0ull, tm = 0ull;
+            if (k != 0x7fffffff) {
+                const ull* row = cur + ((size_t)((k >> 8) - f0) * Q + q) * B * 2;
+                fm = row[2 * (k & 255) + 1];
+                tm = row[2 * (B - 1) + 1] - fm;
+            }
+            rank_best[2 + 2 * q] = fm;
+            rank_best[3 + 2 * q] = tm;
+        }
+        return;
+    }
+    if (threadIdx.x == 0) {
         SplitRec rec;
         if (fk == 0x7fffffff || fb == -INFINITY) {
             rec.feature = -1;
@@ -1151,16 +1182,61 @@ __global__ void __launch_bounds__(kScoreWarps * 32) score_kernel(int level, int3
             rec.score = fb;
         }
         ts->split[level] = rec;
-        ts->score_done = 0;
     }
 }
 
-void launch_score(int level, int32_t F, int32_t B, const ull* cur, const int32_t* border_counts,
-                  double l2, int score_fn, double* grp_score, int32_t* grp_bin, TreeState* ts,
-                  cudaStream_t st) {
+void launch_score(int level, int32_t Fs, int32_t f0, int32_t F, int32_t B, const ull* cur,
+                  const int32_t* border_counts, double l2, int score_fn, double* grp_score, int32_t* grp_bin,
+                  TreeState* ts, ull* rank_best, cudaStream_t st) {
     const unsigned G = (unsigned)((B - 1 + 31) / 32);  // border groups: borders <= B - 1
-    score_kernel<<<dim3(G > 0 ? G : 1, (unsigned)F), kScoreWarps * 32, 0, st>>>(
-        level, F, B, cur, border_counts, l2, score_fn, grp_score, grp_bin, ts);
+    score_kernel<<<dim3(G > 0 ? G : 1, (unsigned)Fs), kScoreWarps * 32, 0, st>>>(
+        level, Fs, f0, F, B, cur, border_counts, l2, score_fn, grp_score, grp_bin, ts, rank_best);
+}
+
+// The winner over the ranks' slice winners, gathered as (score bits, key,
+// per-leaf (false, true) weight sums) records of `stride` words: max score,
+// then lowest key, as the single-device scan would pick.  When a next level
+// follows, small_side[q] = 1 when leaf q's true child carries no more weight
+// than its false child (the rows to histogram; which child is built changes
+// no result, the sums are exact), replacing an all-reduce of child counts.
+__global__ void select_split_kernel(int level, int world, int stride, const ull* __restrict__ all_best,
+                                    TreeState* ts, uint8_t* __restrict__ small_side) {
+    __shared__ int s_r;
+    if (threadIdx.x == 0) {
+        double fb = -INFINITY;
+        int fk = 0x7fffffff, fr = -1;
+        for (int r = 0; r < world; ++r) {
+            const double sc = __longlong_as_double((long long)all_best[(size_t)r * stride]);
+            const int key = (int)(uint32_t)all_best[(size_t)r * stride + 1];
+            if (key == 0x7fffffff) continue;
+            if (better(sc, key, fb, fk)) { fb = sc; fk = key; fr = r; }
+        }
+        SplitRec rec;
+        if (fk == 0x7fffffff || fb == -INFINITY) {
+            rec.feature = -1;
+            rec.bin = -1;
+            rec.score = -INFINITY;
+            atomicOr(&ts->err, kErrNoCandidate);
+            fr = -1;
+        } else {
+            rec.feature = fk >> 8;
+            rec.bin = fk & 255;
+            rec.score = fb;
+        }
+        ts->split[level] = rec;
+        s_r = fr;
+    }
+    __syncthreads();
+    if (!small_side) return;
+    const int Q = 1 << level;
+    const ull* m = s_r >= 0 ? all_best + (size_t)s_r * stride + 2 : nullptr;
+    for (int q = threadIdx.x; q < Q; q += blockDim.x)
+        small_side[q] = m ? (m[2 * q + 1] <= m[2 * q] ? 1 : 0) : 1;
+}
+
+void launch_select_split(int level, int world, int stride, const ull* all_best, TreeState* ts,
+                         uint8_t* small_side, cudaStream_t st) {
+    select_split_kernel<<<1, 256, 0, st>>>(level, world, stride, all_best, ts, small_side);
 }
 
 // ============================================================================

@@ -116,11 +116,19 @@ void launch_hist(const uint8_t* bins_rm, int32_t F_pad, int32_t F, int32_t B, co
 void launch_make_chunks(int level, uint32_t* seg_off, uint32_t* seg_cnt, uint32_t* mem_start,
                         uint32_t* mem_leaf, const uint8_t* small_side, int64_t n_level0,
                         HistChunk* chunks, uint32_t cap, uint32_t* n_chunks, TreeState* ts, cudaStream_t st);
-void launch_derive_prefix(int level, int32_t F, int32_t B, const ull* built, const ull* prev,
+// Derive and score work on this rank's feature slice [f0, f0 + Fs) in
+// feature-major layouts (see derive_prefix_kernel).  With rank_best null the
+// winner goes to ts->split[level]; otherwise the slice winner's record goes to
+// rank_best (score bits, key, then 2^level (false, true) weight sums) for
+// launch_select_split after an all-gather (records of `stride` words; a null
+// small_side skips the next level's build-side choice).
+void launch_derive_prefix(int level, int32_t Fs, int32_t B, const ull* built, const ull* prev,
                           ull* cur, const uint8_t* small_side, cudaStream_t st);
-void launch_score(int level, int32_t F, int32_t B, const ull* cur, const int32_t* border_counts,
-                  double l2, int score_fn, double* feat_score, int32_t* feat_bin, TreeState* ts,
-                  cudaStream_t st);
+void launch_score(int level, int32_t Fs, int32_t f0, int32_t F, int32_t B, const ull* cur,
+                  const int32_t* border_counts, double l2, int score_fn, double* grp_score, int32_t* grp_bin,
+                  TreeState* ts, ull* rank_best, cudaStream_t st);
+void launch_select_split(int level, int world, int stride, const ull* all_best, TreeState* ts,
+                         uint8_t* small_side, cudaStream_t st);
 // flags: 2 * (ceil(n / 32) + 1) words (the split outcome bits, natural then position order); blk_true: ceil(n / kPartTile) + 1; child_cnt: 2^(level+1) (false counts, then true).
 void launch_partition(int level, int64_t n, const uint8_t* bins_fm, int64_t n_stride,
                       const uint32_t* perm, uint32_t* perm_next, SegTables& sg, uint32_t* blk_true,

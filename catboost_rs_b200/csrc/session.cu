@@ -160,6 +160,10 @@ struct cbgpu_session {
     uint32_t* d_err = nullptr;
     void* leaf_export = nullptr;
     size_t built_cells = 0, hist_cells = 0;
+    // Feature slice owned by this rank for derive / score: [f0, f0 + Fs) of the
+    // world * Fs padded features (features >= F have no borders).
+    int Fs = 0, f0 = 0;
+    ull* best_all = nullptr;  // per rank: slice winner record for the all-gather
 
     // host state
     HostRng rng;
@@ -271,13 +275,16 @@ int alloc_session(cbgpu_session* s, const cbgpu_begin_args* a) {
     s->chunk_cap = (size_t)(n / kChunkRows) + (L / 2) + 2;
     DA(s->chunks, s->chunk_cap);
     DA(s->n_chunks, 1);
-    s->built_cells = (size_t)(L / 2 > 0 ? L / 2 : 1) * s->F * s->B * 2;
-    s->hist_cells = (size_t)(L / 2 > 0 ? L / 2 : 1) * s->F * s->B * 2;
+    s->Fs = (s->F + s->world - 1) / s->world;
+    s->f0 = s->rank * s->Fs;
+    s->built_cells = (size_t)(L / 2 > 0 ? L / 2 : 1) * s->world * s->Fs * s->B * 2;
+    s->hist_cells = (size_t)(L / 2 > 0 ? L / 2 : 1) * s->Fs * s->B * 2;
     DA(s->built, s->built_cells);
     DA(s->hist[0], s->hist_cells);
     DA(s->hist[1], s->hist_cells);
-    DA(s->feat_score, (size_t)s->F * 8);  // per (feature, 32-border group) winners
-    DA(s->feat_bin, (size_t)s->F * 8);
+    DA(s->feat_score, (size_t)s->Fs * 8);  // per (feature, 32-border group) winners of the slice
+    DA(s->feat_bin, (size_t)s->Fs * 8);
+    DA(s->best_all, (size_t)(2 + L) * s->world);  // per rank: score, key, 2 * 2^level weight sums
     DA(s->leaf_sums, 2 * L);
     DA(s->leaf_raw, L);
     DA(s->leaf_lrv, L);
@@ -321,7 +328,7 @@ void free_session(cbgpu_session* s) {
     void* ptrs[] = {s->bins_rm, s->bins_fm, s->d_border_counts, s->target, s->weight, s->approx,
                     s->wd1, s->qstats, s->sw32, s->sw64, s->mvs_thr, s->leaf, s->perm[0], s->perm[1],
                     s->seg_mem, s->blk_true, s->child_cnt, s->flags, s->small_side, s->chunks, s->n_chunks, s->built,
-                    s->hist[0], s->hist[1], s->feat_score, s->feat_bin, s->leaf_sums, s->leaf_raw,
+                    s->hist[0], s->hist[1], s->feat_score, s->feat_bin, s->best_all, s->leaf_sums, s->leaf_raw,
                     s->leaf_lrv, s->ts, s->d_err, s->leaf_export};
     for (void* p : ptrs)
         if (p) cudaFree(p);
@@ -357,6 +364,21 @@ template <typename T>
 int allreduce(cbgpu_session* s, T* buf, size_t count, ncclDataType_t dt, ncclRedOp_t op) {
     if (s->world <= 1 || count == 0) return CBGPU_OK;
     NC(ncclAllReduce(buf, buf, count, dt, op, s->comm, s->st));
+    return CBGPU_OK;
+}
+
+// In place: buf holds world equal pieces of `per_rank` elements; afterwards
+// piece `rank` holds the sum over ranks of that piece.
+int reduce_scatter_u64(cbgpu_session* s, ull* buf, size_t per_rank) {
+    if (s->world <= 1 || per_rank == 0) return CBGPU_OK;
+    NC(ncclReduceScatter(buf, buf + (size_t)s->rank * per_rank, per_rank, ncclUint64, ncclSum, s->comm, s->st));
+    return CBGPU_OK;
+}
+
+// In place: piece `rank` of buf (per_rank elements) is sent to every rank.
+int all_gather_u64(cbgpu_session* s, ull* buf, size_t per_rank) {
+    if (s->world <= 1 || per_rank == 0) return CBGPU_OK;
+    NC(ncclAllGather(buf + (size_t)s->rank * per_rank, buf, per_rank, ncclUint64, s->comm, s->st));
     return CBGPU_OK;
 }
 
@@ -520,11 +542,13 @@ int grow(cbgpu_session* s, const double* approx_h, const double* target_h, int64
     // ---- level loop
     int cur = 0;
     int pp = 0;  // current perm buffer
-    const size_t row_cells = (size_t)s->F * s->B * 2;
     for (int l = 0; l < D; ++l) {
         const int e = 2 + 5 * l;
         const size_t built_slots = l == 0 ? 1 : (size_t)1 << (l - 1);
-        CU(cudaMemsetAsync(s->built, 0, sizeof(ull) * built_slots * row_cells, st));
+        // built is feature-major [world * Fs][slot][B][2], so each rank's
+        // feature slice is one contiguous piece for the reduce-scatter
+        const size_t slice_cells = (size_t)s->Fs * built_slots * s->B * 2;
+        CU(cudaMemsetAsync(s->built, 0, sizeof(ull) * slice_cells * s->world, st));
         const uint32_t max_chunks =
             (uint32_t)(s->n / kChunkRows + (l == 0 ? 1 : (1u << (l - 1))) + 1);
         launch_make_chunks(l, s->sg.seg_off, s->sg.seg_cnt, s->sg.mem_start, s->sg.mem_leaf,
@@ -532,28 +556,39 @@ int grow(cbgpu_session* s, const double* approx_h, const double* target_h, int64
                            s->ts, st);
         rec(e);
         launch_hist(s->bins_rm, s->F_pad, s->F, s->B, s->qstats, l == 0 ? nullptr : s->perm[pp], s->chunks,
-                    s->n_chunks, max_chunks, s->built, (int64_t)s->B * 2, (int64_t)s->F * s->B * 2, st);
+                    s->n_chunks, max_chunks, s->built, (int64_t)built_slots * s->B * 2, (int64_t)s->B * 2, st);
         rec(e + 1);
         launches += 2;
         {
-            int rc = allreduce(s, s->built, built_slots * row_cells, ncclUint64, ncclSum);
+            int rc = reduce_scatter_u64(s, s->built, slice_cells);
             if (rc) return rc;
         }
         rec(e + 2);
-        launch_derive_prefix(l, s->F, s->B, s->built, s->hist[cur ^ 1], s->hist[cur], s->small_side, st);
-        launch_score(l, s->F, s->B, s->hist[cur], s->d_border_counts, s->l2, s->score_fn, s->feat_score,
-                     s->feat_bin, s->ts, st);
+        const ull* built_slice = s->built + (size_t)s->rank * slice_cells;
+        launch_derive_prefix(l, s->Fs, s->B, built_slice, s->hist[cur ^ 1], s->hist[cur], s->small_side, st);
+        const int stride = 2 + 2 * (1 << l);  // all-gather record: score, key, (false, true) per leaf
+        launch_score(l, s->Fs, s->f0, s->F, s->B, s->hist[cur], s->d_border_counts, s->l2, s->score_fn,
+                     s->feat_score, s->feat_bin, s->ts,
+                     s->world > 1 ? s->best_all + (size_t)stride * s->rank : nullptr, st);
         launches += 2;
+        if (s->world > 1) {
+            int rc = all_gather_u64(s, s->best_all, (size_t)stride);
+            if (rc) return rc;
+            // also picks the next level's build side: no child-count all-reduce
+            launch_select_split(l, s->world, stride, s->best_all, s->ts, l + 1 < D ? s->small_side : nullptr, st);
+            ++launches;
+        }
         rec(e + 3);
         if (l + 1 < D) {
             launch_partition(l, s->n, s->bins_fm, s->n_stride, l == 0 ? nullptr : s->perm[pp],
                              s->perm[pp ^ 1], s->sg, s->blk_true, s->flags, s->child_cnt, s->ts, st);
             pp ^= 1;
             rec(e + 4);
-            int rc = allreduce(s, s->child_cnt, (size_t)2 << l, ncclUint32, ncclSum);
-            if (rc) return rc;
-            launch_small_side(l + 1, s->child_cnt, s->small_side, st);
-            launches += 5;
+            if (s->world == 1) {  // multi-rank fits chose the build side in select_split
+                launch_small_side(l + 1, s->child_cnt, s->small_side, st);
+                ++launches;
+            }
+            launches += 4;
         } else {
             CU(cudaMemsetAsync(s->leaf_sums, 0, sizeof(ull) * 2 * L, st));
             launch_route_leafsum(D, s->n, s->bins_fm, s->n_stride, s->leaf, s->wd1, s->weight, s->ts,
