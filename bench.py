@@ -291,21 +291,19 @@ def main():
     rt.set_profiling(True)  # per-kernel CUDA events; read after each tree's final sync
     for _ in range(args.warmup):
         rt.grow_tree_on_device(None, y, [], leaf_of_bytes=0, resident_approx=True)
-    hist_ms = rows = launches = 0.0
-    stage = np.zeros(8)
+    rt.timing_sum(reset=True)  # drop the warm-up trees
     barrier()
     with ClockSampler(local_rank) as clk:
         rt.mark(0)
         for _ in range(args.steps):
             rt.grow_tree_on_device(None, y, [], leaf_of_bytes=0, resident_approx=True)
-            tm = rt.timing()
-            stage += tm
-            hist_ms += tm[1]
-            rows += tm[6]
-            launches += tm[7]
         rt.mark(1)
         elapsed = rt.elapsed_ms(0, 1)
         barrier()
+    # per-stage sums over the timed trees (each tree's event times are read
+    # during the next tree's device work, so the loop above has no host reads)
+    stage = rt.timing_sum()
+    hist_ms, rows, launches = stage[1], stage[6], stage[7]
     elapsed = max_over_ranks(elapsed)
     rt.end_device_training()
     value = args.steps / (elapsed / 1e3)

@@ -173,7 +173,17 @@ struct cbgpu_session {
     double prev_mean = 0.0;
     int64_t trees = 0;
     bool profiling = false;
-    cudaEvent_t ev[2 + 5 * 16 + 1] = {};
+    // Per-tree CUDA events, two sets: a tree records into one set while the
+    // previous tree's times are read from the other, during this tree's
+    // device work instead of between trees.
+    static constexpr int kEv = 2 + 5 * 16 + 1;
+    cudaEvent_t ev[2][kEv] = {};
+    int ev_set = 0;                       // set of the tree grown last
+    bool ev_pending[2] = {false, false};  // a finished tree whose times are unread
+    int ev_depth[2] = {0, 0};
+    bool ev_prof[2] = {false, false};
+    double ev_host[2][2] = {};            // rows histogrammed, kernels launched
+    double timing_sum[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     cudaEvent_t uev[4] = {};
     double timing[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     TreeState h_ts{};
@@ -304,7 +314,8 @@ int alloc_session(cbgpu_session* s, const cbgpu_begin_args* a) {
             CU(cudaStreamSynchronize(s->st));
         }
     }
-    for (auto& e : s->ev) CU(cudaEventCreate(&e));
+    for (auto& set : s->ev)
+        for (auto& e : set) CU(cudaEventCreate(&e));
     for (auto& e : s->uev) CU(cudaEventCreate(&e));
     if (s->world > 1) {
         ncclUniqueId id;
@@ -332,8 +343,9 @@ void free_session(cbgpu_session* s) {
                     s->leaf_lrv, s->ts, s->d_err, s->leaf_export};
     for (void* p : ptrs)
         if (p) cudaFree(p);
-    for (auto& e : s->ev)
-        if (e) cudaEventDestroy(e);
+    for (auto& set : s->ev)
+        for (auto& e : set)
+            if (e) cudaEventDestroy(e);
     for (auto& e : s->uev)
         if (e) cudaEventDestroy(e);
     if (s->comm) ncclCommDestroy(s->comm);
@@ -382,10 +394,35 @@ int all_gather_u64(cbgpu_session* s, ull* buf, size_t per_rank) {
     return CBGPU_OK;
 }
 
-float ev_ms(cbgpu_session* s, int a, int b) {
+float ev_ms(cbgpu_session* s, int set, int a, int b) {
     float ms = 0.f;
-    cudaEventElapsedTime(&ms, s->ev[a], s->ev[b]);
+    cudaEventElapsedTime(&ms, s->ev[set][a], s->ev[set][b]);
     return ms;
+}
+
+// Reads a finished tree's event times into timing (that tree) and timing_sum.
+void collect_timing(cbgpu_session* s, int set) {
+    if (!s->ev_pending[set]) return;
+    s->ev_pending[set] = false;
+    const int D = s->ev_depth[set];
+    double t[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    t[0] = ev_ms(s, set, 0, 2 + 5 * D);
+    if (s->ev_prof[set]) {
+        for (int l = 0; l < D; ++l) {
+            const int e = 2 + 5 * l;
+            t[1] += ev_ms(s, set, e, e + 1);
+            t[5] += ev_ms(s, set, e + 1, e + 2);
+            t[2] += ev_ms(s, set, e + 2, e + 3);
+            t[3] += ev_ms(s, set, e + 3, e + 4);
+        }
+        t[4] = ev_ms(s, set, 0, 1);
+    }
+    t[6] = s->ev_host[set][0];
+    t[7] = s->ev_host[set][1];
+    for (int k = 0; k < 8; ++k) {
+        s->timing[k] = t[k];
+        s->timing_sum[k] += t[k];
+    }
 }
 
 // First-tree MVS lambda (bootstrap.rs:358-376): (sum |w*der1| / n)^2 with a
@@ -466,7 +503,8 @@ int grow(cbgpu_session* s, const double* approx_h, const double* target_h, int64
     const bool prof = s->profiling;
     int launches = 0;
     // event slots: 0 tree start, 1 after derivatives, per level l: 2+5l .. 6+5l, last: 2+5D
-    auto rec = [&](int k) { if (prof || k == 0 || k == 2 + 5 * D) cudaEventRecord(s->ev[k], st); };
+    const int set = s->ev_set ^ 1;  // the other set may still hold the previous tree's unread times
+    auto rec = [&](int k) { if (prof || k == 0 || k == 2 + 5 * D) cudaEventRecord(s->ev[set][k], st); };
 
     rec(0);
     if (!s->target_ready) {
@@ -613,8 +651,32 @@ int grow(cbgpu_session* s, const double* approx_h, const double* target_h, int64
         CU(cudaMemcpyAsync(leaf_of, s->leaf_export, (size_t)leaf_of_bytes * s->n, cudaMemcpyDeviceToHost, st));
     }
     rec(2 + 5 * D);
+    // Host work that needs no device result runs while the tree executes: the
+    // previous tree's event times, and the RNG phase after the tree
+    // (boosting.rs:7267-7300 + device_draw_replay.rs), which depends only on
+    // the depth and the feature count.
+    collect_timing(s, set ^ 1);
+    if (!s->sample_from_host && s->boot != CBGPU_BOOT_NO) {
+        for (int l = 0; l < D; ++l) {
+            for (int f = 0; f < s->F; ++f) (void)s->rng.real1();
+            (void)s->rng.gen();
+            for (int f = 0; f < s->F; ++f) (void)s->rng.std_normal();
+        }
+        s->rng.gen();  // POST_TREE_EXTRA_DRAWS = 2
+        s->rng.gen();
+    }
     CU(cudaStreamSynchronize(st));
     CU(cudaGetLastError());
+    s->ev_set = set;
+    s->ev_pending[set] = true;
+    s->ev_depth[set] = D;
+    s->ev_prof[set] = prof;
+    {
+        double rows = 0;
+        for (int l = 0; l < D; ++l) rows += (double)s->h_ts.hist_rows[l];
+        s->ev_host[set][0] = rows;
+        s->ev_host[set][1] = (double)launches;
+    }
     if (s->h_ts.err) {
         if (s->h_ts.err & kErrNoCandidate)
             return fail(CBGPU_ERR_DEVICE, "Degenerate: no split candidate available");
@@ -628,16 +690,6 @@ int grow(cbgpu_session* s, const double* approx_h, const double* target_h, int64
     if (n_splits) *n_splits = D;
     if (leaf_values) memcpy(leaf_values, raw.data(), sizeof(double) * L);
     s->pending = true;
-    // RNG phase after the tree (boosting.rs:7267-7300 + device_draw_replay.rs)
-    if (!s->sample_from_host && s->boot != CBGPU_BOOT_NO) {
-        for (int l = 0; l < D; ++l) {
-            for (int f = 0; f < s->F; ++f) (void)s->rng.real1();
-            (void)s->rng.gen();
-            for (int f = 0; f < s->F; ++f) (void)s->rng.std_normal();
-        }
-        s->rng.gen();  // POST_TREE_EXTRA_DRAWS = 2
-        s->rng.gen();
-    }
     // last_iter_mean_leaf_value over the learning-rate-scaled leaves (bootstrap.rs:382-389)
     double acc = 0.0;
     for (int k = 0; k < L; ++k) {
@@ -647,27 +699,6 @@ int grow(cbgpu_session* s, const double* approx_h, const double* target_h, int64
     s->prev_mean = acc / (double)L;
     s->has_prev_mean = true;
     s->trees++;
-    // timing
-    s->timing[0] = ev_ms(s, 0, 2 + 5 * D);
-    double rows = 0;
-    for (int l = 0; l < D; ++l) rows += (double)s->h_ts.hist_rows[l];
-    s->timing[6] = rows;
-    s->timing[7] = (double)launches;
-    if (prof) {
-        double th = 0, tsc = 0, tp = 0, tc = 0;
-        for (int l = 0; l < D; ++l) {
-            const int e = 2 + 5 * l;
-            th += ev_ms(s, e, e + 1);
-            tc += ev_ms(s, e + 1, e + 2);
-            tsc += ev_ms(s, e + 2, e + 3);
-            tp += ev_ms(s, e + 3, e + 4);
-        }
-        s->timing[1] = th;
-        s->timing[2] = tsc;
-        s->timing[3] = tp;
-        s->timing[4] = ev_ms(s, 0, 1);
-        s->timing[5] = tc;
-    }
     return CBGPU_OK;
 }
 
@@ -829,7 +860,21 @@ int cbgpu_session_last_sample(cbgpu_session* s, double* out, int64_t n) {
 
 int cbgpu_session_timing(cbgpu_session* s, double* out8) {
     if (!s || !out8) return fail(CBGPU_ERR_INVALID, "bad arguments");
+    CU(cudaSetDevice(s->device));
+    collect_timing(s, s->ev_set);  // the last tree's events completed when its grow returned
     for (int k = 0; k < 8; ++k) out8[k] = s->timing[k];
+    return CBGPU_OK;
+}
+
+int cbgpu_session_timing_sum(cbgpu_session* s, double* out8, int32_t reset) {
+    if (!s || !out8) return fail(CBGPU_ERR_INVALID, "bad arguments");
+    CU(cudaSetDevice(s->device));
+    collect_timing(s, s->ev_set ^ 1);
+    collect_timing(s, s->ev_set);
+    for (int k = 0; k < 8; ++k) {
+        out8[k] = s->timing_sum[k];
+        if (reset) s->timing_sum[k] = 0.0;
+    }
     return CBGPU_OK;
 }
 

@@ -253,6 +253,12 @@ class B200Runtime:
         _lib.check(self._L.cbgpu_session_timing(self._s, _ptr(out)))
         return out
 
+    def timing_sum(self, reset: bool = False) -> np.ndarray:
+        """The timing() figures summed over the trees since the last reset."""
+        out = np.zeros(8, dtype=np.float64)
+        _lib.check(self._L.cbgpu_session_timing_sum(self._s, _ptr(out), 1 if reset else 0))
+        return out
+
     def mark(self, slot: int) -> None:
         """Record user event `slot` (0..3) on the session stream."""
         _lib.check(self._L.cbgpu_session_mark(self._s, slot))

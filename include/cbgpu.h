@@ -171,6 +171,13 @@ CBGPU_API int cbgpu_session_last_sample(cbgpu_session* s, double* out, int64_t n
  * [6] rows histogrammed over all levels and [7] kernels launched. */
 CBGPU_API int cbgpu_session_timing(cbgpu_session* s, double* out8);
 
+/* The same eight figures summed over every tree since the last reset (reset
+ * != 0 zeroes the sums after reading).  Reading a tree's event times happens
+ * during the next tree's device work, so a loop that only reads the sum at
+ * its end adds no host time between trees.  No counterpart in the reference
+ * (the reference reports stage times through its own profiler). */
+CBGPU_API int cbgpu_session_timing_sum(cbgpu_session* s, double* out8, int32_t reset);
+
 /* Record user event `slot` (0..3) on the session's stream, and read the
  * device milliseconds between two recorded slots (synchronizes on `b`). */
 CBGPU_API int cbgpu_session_mark(cbgpu_session* s, int32_t slot);

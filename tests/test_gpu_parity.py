@@ -298,3 +298,34 @@ def test_begin_u32_bins_path_matches_raw_path():
         assert [s[1] for s in tree.splits] == list(ref.split_bin[it])
     np.testing.assert_array_equal(rt.resident_approx(), ref.staged[-1])
     rt.end_device_training()
+
+
+def test_timing_sum_matches_per_tree_timing():
+    """cbgpu_session_timing_sum adds up the per-tree figures whether or not
+    each tree's timing was read in between (reads are deferred to the next
+    tree's device work)."""
+    X, y, borders = make_dataset(20000, 12, seed=8, border_count=32)
+    nb = max(len(b) for b in borders) + 1
+    per_tree, sums = [], []
+    for read_each in (True, False):
+        rt = cb.B200Runtime()
+        cfg = cb.DeviceTrainConfig(bootstrap_type="Bayesian", rng_seed=4)
+        assert rt.begin_device_training_raw("RMSE", 6, True, 1, "Cosine", _cols(X), borders, None, X.shape[0],
+                                            X.shape[1], nb, 0.1, 3.0, cfg)
+        rt.set_profiling(True)
+        rt.timing_sum(reset=True)
+        rows = []
+        for _ in range(4):
+            rt.grow_tree_on_device(None, y, [], leaf_of_bytes=0, resident_approx=True)
+            if read_each:
+                rows.append(rt.timing().copy())
+        tot = rt.timing_sum()
+        rt.end_device_training()
+        if read_each:
+            per_tree = np.array(rows)
+            np.testing.assert_allclose(tot, per_tree.sum(axis=0), rtol=1e-12)
+        sums.append(tot)
+    # histogrammed rows and launch counts are exact and identical either way
+    assert sums[0][6] == sums[1][6] == per_tree[:, 6].sum()
+    assert sums[0][7] == sums[1][7]
+    assert (sums[1][:6] >= 0).all() and sums[1][0] > 0 and sums[1][1] > 0
