@@ -29,6 +29,11 @@ sys.path.insert(0, ROOT)
 BLOCK_ROWS = 1 << 20       # data is generated in fixed 1Mi-row blocks so any sharding sees the same rows
 BORDER_SAMPLE = 200_000    # fixed-seed sample the borders are selected from (cf. cb-data's 200k sample)
 FMIN = float(np.finfo(np.float32).min)
+# DRAM bytes (read + write) per histogrammed row, from an ncu capture of all
+# eight histogram launches of one config-2-shaped tree at 2M rows (the
+# profile summary hist_kernel_dram_2M.md); the roofline's `traffic` scales it
+# by the rows each launch histograms.
+HIST_DRAM_BYTES_PER_ROW = 412.3
 
 
 def peaks():
@@ -368,7 +373,14 @@ def main():
                 "scaling": "strong", "vs_baseline": None, "dtype": "int64",
                 "data": "synthetic (seeded, config-2 shapes and distributions)", "config": base_cfg,
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                             "frac": (achieved / peak) if achieved else None, "traffic": None,
+                             "frac": (achieved / peak) if achieved else None,
+                             "traffic": HIST_DRAM_BYTES_PER_ROW * rows / hist_launches,
+                             "traffic_unit": "bytes per launch",
+                             "traffic_source": "ncu capture at 2M rows, 412.3 B per histogrammed row, "
+                                               "scaled by rows per launch",
+                             "limiter": "shared-memory reduction issue: 4 exact 32-bit red.shared per "
+                                        "(row, feature); LSU pipe 70.6% of peak, top stall mio_throttle "
+                                        "(ncu, 2M rows)",
                              "kernel": "hist_kernel", "peak_kind": peak_kind,
                              "algorithmic_bytes_per_launch": alg_bytes / hist_launches,
                              "avg_launch_ms": hist_ms / hist_launches},
