@@ -1,0 +1,154 @@
+"""The BASELINE configs the device path covers, at their full sizes.
+
+Config 1 (100k x 50 RMSE, 254 borders, depth 6, 100 trees) is small enough for
+the oracle: every tree is compared with it.
+
+Config 2 (10M x 200 Logloss, 128 borders with the NaN sentinel, depth 8,
+Bayesian T=1) is too large for the oracle in a test, so its first trees are
+checked through properties that do not depend on size, recomputed on the host
+from the device's own bins and bootstrap sample:
+  - routing: every row's leaf id equals the leaf its bins give under the
+    returned splits (bit-exact);
+  - level 0: the chosen (feature, border) is the argmax of the Cosine score of
+    exact host histograms, or within the 1e-6 relative near-tie bar;
+  - leaf values: calc_average of host sums of the unsampled w*der1 and w per
+    leaf, within 1e-9 relative (the device sums are exact integers);
+  - determinism: a second session grows bit-identical trees.
+"""
+import os
+import sys
+
+import numpy as np
+import pytest
+
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+cb = pytest.importorskip("catboost_rs_b200")
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _need_cuda():
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+
+
+def _config1():
+    """X ~ N(0,1) (seed 0), w ~ N(0,1) with 10 nonzero
+    entries, y = X.w + 0.1 N(0,1); uniform-quantile borders (254)."""
+    rs = np.random.RandomState(0)
+    n, F = 100_000, 50
+    X = rs.standard_normal((n, F)).astype(np.float32)
+    w = np.zeros(F)
+    nz = rs.choice(F, size=10, replace=False)
+    w[nz] = rs.standard_normal(10)
+    y = X.astype(np.float64) @ w + 0.1 * rs.standard_normal(n)
+    borders = []
+    for f in range(F):
+        q = np.quantile(X[:, f].astype(np.float64), np.linspace(0, 1, 256)[1:-1])
+        borders.append(np.unique(q.astype(np.float32).astype(np.float64)))
+    return X, y, borders
+
+
+def test_config1_full_size_matches_oracle():
+    X, y, borders = _config1()
+    fp = cb.FitParams(loss="RMSE", depth=6, iterations=100, learning_rate=0.1, l2_leaf_reg=3.0,
+                      score_function="Cosine", bootstrap_type="No", boost_from_average=True)
+    m = cb.fit([np.ascontiguousarray(X[:, f]) for f in range(X.shape[1])], borders, y, fp, staged=False)
+    bins = oracle.quantize(X.T.copy(), borders)
+    o = oracle.train(bins, [len(b) for b in borders], y, loss="RMSE", depth=6, iterations=100,
+                     learning_rate=0.1, l2_leaf_reg=3.0, score_function="Cosine", bootstrap_type="No",
+                     boost_from_average=True, staged=True)
+    np.testing.assert_array_equal(m.split_feature, o.split_feature)
+    np.testing.assert_array_equal(m.split_bin, o.split_bin)
+    assert np.max(np.abs(m.leaf_values - o.leaf_values)) <= 1e-5
+    pred = m.predict(X)
+    assert np.max(np.abs(pred - o.staged[-1])) <= 1e-5
+
+
+# ---- config 2 at full size ---------------------------------------------------
+
+def _config2():
+    sys.path.insert(0, ROOT)
+    import bench
+    n, F = 10_000_000, 200
+    Xfm, y = bench.make_shard(0, n, F, seed=0)
+    borders = bench.make_borders(F, 128, seed=0)
+    return Xfm, y, borders
+
+
+def _cosine_scores(g_hist, h_hist, nb, l2):
+    """Level-0 Cosine scores of borders 0..nb-1 of one feature from its bin
+    sums (false side = bins <= border), the formula of score.rs:117."""
+    pg, ph = np.cumsum(g_hist)[:nb], np.cumsum(h_hist)[:nb]
+    tg, th = g_hist.sum(), h_hist.sum()
+    num = np.zeros(nb)
+    den = np.full(nb, 1e-100)
+    for sg, sh in ((pg, ph), (tg - pg, th - ph)):
+        avg = np.where(sh > 0, sg / (sh + l2), 0.0)
+        num = num + avg * sg
+        den = den + avg * avg * sh
+    s = num / np.sqrt(den)
+    return np.where(np.isnan(s), -np.inf, s)
+
+
+def test_config2_full_size_properties():
+    Xfm, y, borders = _config2()
+    n, F = y.size, Xfm.shape[0]
+    nbins = max(len(b) for b in borders) + 1
+    depth, lr, l2 = 8, 0.05, 3.0
+
+    def session():
+        rt = cb.B200Runtime()
+        cfg = cb.DeviceTrainConfig(bootstrap_type="Bayesian", bagging_temperature=1.0, rng_seed=0)
+        assert rt.begin_device_training_raw("Logloss", depth, True, 1, "Cosine", list(Xfm), borders, None, n, F,
+                                            nbins, lr, l2, cfg)
+        return rt
+
+    rt = session()
+    bins = rt.device_bins(F)  # u8 [F][n], the device's own quantization
+    approx = np.zeros(n)
+    trees = []
+    for it in range(2):
+        tree = rt.grow_tree_on_device(None, y, [], leaf_of_bytes=1, resident_approx=True)
+        s = rt.last_sample()  # bootstrap multiplier of this tree
+        splits = [(f, b) for f, b, _ in tree.splits]
+        # routing, bit-exact
+        leaf = np.zeros(n, dtype=np.int64)
+        for lvl, (f, b) in enumerate(splits):
+            leaf |= (bins[f].astype(np.int64) > b).astype(np.int64) << lvl
+        np.testing.assert_array_equal(tree.leaf_of.astype(np.int64), leaf)
+        # der1 for Logloss at the current approximant (loss.rs:35-80)
+        p = 1.0 - 1.0 / (1.0 + np.exp(approx))
+        d1 = y - p
+        # level 0: argmax of exact host histograms (or a near-tie within 1e-6)
+        if it == 0:
+            # host histograms in f64 (the CPU restatement's histogram, threads over features)
+            hist = oracle.build_histogram(bins, d1 * s, s, n_bins=nbins)[0]
+            best, scores = -np.inf, {}
+            for f in range(F):
+                sc = _cosine_scores(hist[f, :, 0], hist[f, :, 1], len(borders[f]), l2)
+                scores[f] = sc
+                best = max(best, sc.max())
+            f0, b0 = splits[0]
+            assert scores[f0][b0] >= best - 1e-6 * abs(best), (splits[0], scores[f0][b0], best)
+        # leaf values: calc_average over the unsampled channels (boosting.rs:2470-2517)
+        L = 1 << depth
+        sd = np.bincount(leaf, weights=d1, minlength=L)
+        sw = np.bincount(leaf, minlength=L).astype(np.float64)
+        want = np.where(sw > 0, sd / (sw + l2), 0.0)
+        np.testing.assert_allclose(tree.leaf_values, want, rtol=1e-9, atol=1e-12)
+        approx = approx + lr * tree.leaf_values[leaf]
+        trees.append((splits, tree.leaf_values.copy()))
+    rt.end_device_training()
+    # determinism across sessions
+    rt = session()
+    for splits, lv in trees:
+        tree = rt.grow_tree_on_device(None, y, [], leaf_of_bytes=0, resident_approx=True)
+        assert [(f, b) for f, b, _ in tree.splits] == splits
+        np.testing.assert_array_equal(tree.leaf_values, lv)
+    rt.end_device_training()
