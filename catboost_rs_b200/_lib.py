@@ -33,7 +33,7 @@ class BeginArgs(C.Structure):
 EXPORTS = [
     "cbgpu_begin", "cbgpu_begin_raw", "cbgpu_grow_tree", "cbgpu_end", "cbgpu_compute_gradients",
     "cbgpu_last_error", "cbgpu_session_approx", "cbgpu_session_bins", "cbgpu_session_last_sample",
-    "cbgpu_session_timing", "cbgpu_session_timing_sum", "cbgpu_session_set_profiling", "cbgpu_session_rng_state",
+    "cbgpu_session_timing", "cbgpu_session_timing_sum", "cbgpu_session_set_profiling", "cbgpu_session_set_graphs", "cbgpu_session_rng_state",
     "cbgpu_histogram", "cbgpu_bootstrap_weights", "cbgpu_nccl_unique_id", "cbgpu_version",
     "cbgpu_session_mark", "cbgpu_session_elapsed_ms", "cbgpu_histogram_noalloc",
 ]
@@ -71,6 +71,7 @@ def load(path: str = LIB_PATH):
         "cbgpu_session_timing": ([vp, vp], C.c_int),
         "cbgpu_session_timing_sum": ([vp, vp, i32], C.c_int),
         "cbgpu_session_set_profiling": ([vp, i32], C.c_int),
+        "cbgpu_session_set_graphs": ([vp, i32], C.c_int),
         "cbgpu_session_rng_state": ([vp, vp], C.c_int),
         "cbgpu_session_mark": ([vp, i32], C.c_int),
         "cbgpu_session_elapsed_ms": ([vp, i32, i32, vp], C.c_int),

@@ -178,8 +178,8 @@ void launch_transpose_rm_to_fm(const uint8_t* rm, int64_t n, int32_t F, int32_t 
 // Bernoulli: the main stream continues across rows: row g uses the base state
 // advanced g draws (set_sampled_control, bootstrap.rs:178-184).  Each thread
 // jumps once and steps kBootRun consecutive rows.
-__global__ void bootstrap_kernel(int mode, int64_t n, int64_t row_offset, uint64_t rand_seed,
-                                 Rng64 base, double rate, float temp, float* __restrict__ out) {
+__global__ void bootstrap_kernel(int mode, int64_t n, int64_t row_offset, const TreeParams* __restrict__ tp,
+                                 double rate, float temp, float* __restrict__ out) {
     static_assert(kBootRun == 8, "a run is stored as two float4");
     int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
     int64_t i0 = t * kBootRun;
@@ -187,6 +187,7 @@ __global__ void bootstrap_kernel(int mode, int64_t n, int64_t row_offset, uint64
     int64_t g0 = row_offset + i0;
     float v[kBootRun];
     if (mode == 1) {
+        const uint64_t rand_seed = tp->boot_seed;
         Rng64 r = Rng64::from_seed(rand_seed + (uint64_t)(g0 / 1000));
         r.advance(10 + (uint64_t)(g0 % 1000));
 #pragma unroll
@@ -199,7 +200,7 @@ __global__ void bootstrap_kernel(int mode, int64_t n, int64_t row_offset, uint64
             v[j] = i0 + j < n ? (float)bayesian_weight(real1(r), temp) : 0.0f;
         }
     } else {
-        Rng64 r = base;
+        Rng64 r = tp->boot_base;
         r.advance((uint64_t)g0);
 #pragma unroll
         for (int j = 0; j < kBootRun; ++j) v[j] = i0 + j < n && real1(r) < rate ? 1.0f : 0.0f;
@@ -212,13 +213,12 @@ __global__ void bootstrap_kernel(int mode, int64_t n, int64_t row_offset, uint64
     }
 }
 
-void launch_bootstrap(int mode, int64_t n, int64_t row_offset, uint64_t rand_seed, Rng64 base,
-                      double rate, float temp, float* out_sw, cudaStream_t st) {
+void launch_bootstrap(int mode, int64_t n, int64_t row_offset, const TreeParams* tp, double rate, float temp,
+                      float* out_sw, cudaStream_t st) {
     int64_t threads = (n + kBootRun - 1) / kBootRun;
     int64_t blocks = (threads + 255) / 256;
     if (blocks < 1) return;
-    bootstrap_kernel<<<(unsigned)blocks, 256, 0, st>>>(mode, n, row_offset, rand_seed, base, rate,
-                                                       temp, out_sw);
+    bootstrap_kernel<<<(unsigned)blocks, 256, 0, st>>>(mode, n, row_offset, tp, rate, temp, out_sw);
 }
 
 // ---- MVS (bootstrap.rs:186-300): per 8192-row block a threshold from the
@@ -231,15 +231,15 @@ constexpr int kMvsThreads = 256;
 __device__ __forceinline__ double mvs_der_obj(double wd) { return sqrt(__dmul_rn(wd, wd)); }
 
 __global__ void __launch_bounds__(kMvsThreads) mvs_threshold_kernel(
-    int64_t n, const double* __restrict__ wd1, double lambda, double rate,
-    double* __restrict__ scratch, double* __restrict__ thresholds) {
+    int64_t n, const double* __restrict__ wd1, const TreeParams* __restrict__ tp, double rate,
+    double* __restrict__ thresholds) {
     extern __shared__ double msm[];
     double* bufA = msm;
     double* bufB = msm + kMvsBlock;
     __shared__ int s_scan[40];
     __shared__ double s_state[4];  // sum_small_cur, n_large_cur, result
     __shared__ int s_ctl[4];       // len, which buffer/offset, done
-    (void)scratch;
+    const double lambda = tp->mvs_lambda;
     const int64_t beg = (int64_t)blockIdx.x * kMvsBlock;
     const int64_t end = beg + kMvsBlock < n ? beg + kMvsBlock : n;
     const int bs = (int)(end - beg);
@@ -334,9 +334,11 @@ __global__ void __launch_bounds__(kMvsThreads) mvs_threshold_kernel(
 }
 
 __global__ void __launch_bounds__(kMvsThreads) mvs_weights_kernel(
-    int64_t n, int64_t row_offset, const double* __restrict__ wd1, double lambda,
-    uint64_t rand_seed, const double* __restrict__ thresholds, float* __restrict__ out) {
+    int64_t n, int64_t row_offset, const double* __restrict__ wd1, const TreeParams* __restrict__ tp,
+    const double* __restrict__ thresholds, float* __restrict__ out) {
     __shared__ int s_scan[40];
+    const double lambda = tp->mvs_lambda;
+    const uint64_t rand_seed = tp->boot_seed;
     const int64_t beg = (int64_t)blockIdx.x * kMvsBlock;
     const int64_t end = beg + kMvsBlock < n ? beg + kMvsBlock : n;
     const int bs = (int)(end - beg);
@@ -369,22 +371,21 @@ __global__ void __launch_bounds__(kMvsThreads) mvs_weights_kernel(
     }
 }
 
-void launch_mvs(int64_t n, int64_t row_offset, const double* wd1, double lambda, double rate,
-                uint64_t rand_seed, double* scratch, double* thresholds, float* out_sw,
-                cudaStream_t st) {
+void launch_mvs(int64_t n, int64_t row_offset, const double* wd1, const TreeParams* tp, double rate,
+                double* thresholds, float* out_sw, cudaStream_t st) {
     int64_t blocks = (n + kMvsBlock - 1) / kMvsBlock;
     if (blocks < 1) return;
     size_t smem = sizeof(double) * 2 * kMvsBlock;
-    static bool attr = false;
-    if (!attr) {
+    static int attr_device = -1;  // the attribute is set per device, before any capture
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (attr_device != dev) {
         cudaFuncSetAttribute(mvs_threshold_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)smem);
-        attr = true;
+        attr_device = dev;
     }
-    mvs_threshold_kernel<<<(unsigned)blocks, kMvsThreads, smem, st>>>(n, wd1, lambda, rate, scratch,
-                                                                       thresholds);
-    mvs_weights_kernel<<<(unsigned)blocks, kMvsThreads, 0, st>>>(n, row_offset, wd1, lambda,
-                                                                  rand_seed, thresholds, out_sw);
+    mvs_threshold_kernel<<<(unsigned)blocks, kMvsThreads, smem, st>>>(n, wd1, tp, rate, thresholds);
+    mvs_weights_kernel<<<(unsigned)blocks, kMvsThreads, 0, st>>>(n, row_offset, wd1, tp, thresholds, out_sw);
 }
 
 // ============================================================================
@@ -432,8 +433,9 @@ constexpr int kDerRows = 4;  // rows per thread per step, loads issued first
 __global__ void __launch_bounds__(256) der_kernel(
     int64_t n, int loss, double* __restrict__ approx, const double* __restrict__ target,
     const double* __restrict__ weight, const uint16_t* __restrict__ leaf,
-    const double* __restrict__ lrv, int s_mode, const float* __restrict__ sw32,
+    const double* __restrict__ lrv_in, const TreeParams* __restrict__ tp, int s_mode, const float* __restrict__ sw32,
     const double* __restrict__ sw64, double* __restrict__ wd1, TreeState* ts, bool defer) {
+    const double* lrv = tp->pending ? lrv_in : nullptr;
     double m[4] = {0.0, 0.0, 0.0, 0.0};
     bool bad = false;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -474,12 +476,12 @@ __global__ void __launch_bounds__(256) der_kernel(
 }
 
 void launch_der(int64_t n, int loss, double* approx, const double* target, const double* weight,
-                const uint16_t* leaf, const double* lrv, int s_mode, const float* sw32,
+                const uint16_t* leaf, const double* lrv, const TreeParams* tp, int s_mode, const float* sw32,
                 const double* sw64, double* wd1, TreeState* ts, bool defer, cudaStream_t st) {
     int64_t blocks = (n + 255) / 256;
     if (blocks > 148 * 8) blocks = 148 * 8;
     if (blocks < 1) blocks = 1;
-    der_kernel<<<(unsigned)blocks, 256, 0, st>>>(n, loss, approx, target, weight, leaf, lrv, s_mode,
+    der_kernel<<<(unsigned)blocks, 256, 0, st>>>(n, loss, approx, target, weight, leaf, lrv, tp, s_mode,
                                                  sw32, sw64, wd1, ts, defer);
 }
 

@@ -35,6 +35,17 @@ struct SplitRec {
 };
 
 // Per-tree device-side results (one D2H per tree).
+// Per-tree scalars the host decides (from its RNG stream replica) and the
+// kernels read from device memory, so a captured tree graph replays with new
+// values: copied host -> device before every tree.
+struct TreeParams {
+    uint64_t boot_seed;  // Bayesian rand_seed / MVS seed
+    Rng64 boot_base;     // Bernoulli: the main stream at the tree's first row
+    double mvs_lambda;
+    int32_t pending;     // apply the previous tree's leaf values before the derivatives
+    int32_t pad;
+};
+
 struct TreeState {
     SplitRec split[16];
     uint32_t err;
@@ -85,15 +96,16 @@ void launch_transpose_rm_to_fm(const uint8_t* rm, int64_t n, int32_t F, int32_t 
                                uint8_t* fm, int64_t n_stride, cudaStream_t st);
 
 // ---- per tree: bootstrap, derivatives, scales -------------------------------
-// mode: 1 = Bayesian (rand_seed, temp), 2 = Bernoulli (base state, rate)
-void launch_bootstrap(int mode, int64_t n, int64_t row_offset, uint64_t rand_seed, Rng64 base,
-                      double rate, float temp, float* out_sw, cudaStream_t st);
-void launch_mvs(int64_t n, int64_t row_offset, const double* wd1, double lambda, double rate,
-                uint64_t rand_seed, double* scratch, double* thresholds, float* out_sw,
-                cudaStream_t st);
-// s_mode: 0 = none (weights 1), 1 = f32 device sample, 2 = f64 host sample
+// mode: 1 = Bayesian (tp->boot_seed, temp), 2 = Bernoulli (tp->boot_base, rate)
+void launch_bootstrap(int mode, int64_t n, int64_t row_offset, const TreeParams* tp, double rate, float temp,
+                      float* out_sw, cudaStream_t st);
+// MVS with lambda tp->mvs_lambda and seed tp->boot_seed
+void launch_mvs(int64_t n, int64_t row_offset, const double* wd1, const TreeParams* tp, double rate,
+                double* thresholds, float* out_sw, cudaStream_t st);
+// s_mode: 0 = none (weights 1), 1 = f32 device sample, 2 = f64 host sample.
+// approx += lrv[leaf] first when tp->pending.
 void launch_der(int64_t n, int loss, double* approx, const double* target, const double* weight,
-                const uint16_t* leaf, const double* pending_lrv, int s_mode, const float* sw32,
+                const uint16_t* leaf, const double* lrv, const TreeParams* tp, int s_mode, const float* sw32,
                 const double* sw64, double* wd1, TreeState* ts, bool defer_gh, cudaStream_t st);
 void launch_max_gh(int64_t n, const double* wd1, const double* weight, const float* sw32, TreeState* ts,
                    cudaStream_t st);

@@ -99,6 +99,25 @@ int dalloc(T** p, size_t count) {
         if (_rc) return _rc;               \
     } while (0)
 
+// Pinned host allocation (device copies into it are asynchronous and graph-capturable).
+template <typename T>
+int halloc(T** p, size_t count) {
+    *p = nullptr;
+    if (count == 0) count = 1;
+    cudaError_t e = cudaMallocHost((void**)p, sizeof(T) * count);
+    if (e != cudaSuccess)
+        return fail(CBGPU_ERR_OOM, "cudaMallocHost(%zu bytes) failed: %s", sizeof(T) * count,
+                    cudaGetErrorString(e));
+    memset((void*)*p, 0, sizeof(T) * count);
+    return CBGPU_OK;
+}
+
+#define HA(p, count)                       \
+    do {                                   \
+        int _rc = halloc(&(p), (count));   \
+        if (_rc) return _rc;               \
+    } while (0)
+
 }  // namespace
 
 namespace cbgpu {
@@ -186,7 +205,16 @@ struct cbgpu_session {
     double timing_sum[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     cudaEvent_t uev[4] = {};
     double timing[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    TreeState h_ts{};
+    TreeState* h_ts = nullptr;  // pinned: the tree's result state
+    double* h_raw = nullptr;     // pinned: the tree's leaf values
+    TreeParams* h_tp = nullptr;  // pinned: per-tree scalars, copied to d_tp before each tree
+    TreeParams* d_tp = nullptr;
+    // Captured tree graphs, one per event set (their event nodes differ), with
+    // the launch shape they were captured for and their kernel count.
+    bool use_graphs = true;
+    cudaGraphExec_t graph[2] = {nullptr, nullptr};
+    int graph_key[2] = {-1, -1};
+    int graph_launches[2] = {0, 0};
 };
 
 namespace {
@@ -300,6 +328,10 @@ int alloc_session(cbgpu_session* s, const cbgpu_begin_args* a) {
     DA(s->leaf_lrv, L);
     DA(s->ts, 1);
     DA(s->d_err, 1);
+    DA(s->d_tp, 1);
+    HA(s->h_ts, 1);
+    HA(s->h_raw, L);
+    HA(s->h_tp, 1);
     CU(cudaMemsetAsync(s->ts, 0, sizeof(TreeState), s->st));
     CU(cudaMemsetAsync(s->d_err, 0, sizeof(uint32_t), s->st));
     CU(cudaMemsetAsync(s->leaf, 0, sizeof(uint16_t) * n, s->st));
@@ -336,13 +368,19 @@ void free_session(cbgpu_session* s) {
         s->comm = nullptr;
     }
     if (s->st) cudaStreamSynchronize(s->st);
+    // graphs hold NCCL work: released before the communicator
+    for (auto& g : s->graph)
+        if (g) cudaGraphExecDestroy(g);
     void* ptrs[] = {s->bins_rm, s->bins_fm, s->d_border_counts, s->target, s->weight, s->approx,
                     s->wd1, s->qstats, s->sw32, s->sw64, s->mvs_thr, s->leaf, s->perm[0], s->perm[1],
                     s->seg_mem, s->blk_true, s->child_cnt, s->flags, s->small_side, s->chunks, s->n_chunks, s->built,
                     s->hist[0], s->hist[1], s->feat_score, s->feat_bin, s->best_all, s->leaf_sums, s->leaf_raw,
-                    s->leaf_lrv, s->ts, s->d_err, s->leaf_export};
+                    s->leaf_lrv, s->ts, s->d_err, s->leaf_export, s->d_tp};
     for (void* p : ptrs)
         if (p) cudaFree(p);
+    void* hptrs[] = {s->h_ts, s->h_raw, s->h_tp};
+    for (void* p : hptrs)
+        if (p) cudaFreeHost(p);
     for (auto& set : s->ev)
         for (auto& e : set)
             if (e) cudaEventDestroy(e);
@@ -470,100 +508,39 @@ int first_mvs_lambda(cbgpu_session* s, const double* approx_h, const double* tar
     return CBGPU_OK;
 }
 
-int grow(cbgpu_session* s, const double* approx_h, const double* target_h, int64_t n,
-         const double* sample, int64_t sample_len, int32_t* split_feature, int32_t* split_bin,
-         int32_t* n_splits, double* leaf_values, void* leaf_of, int32_t leaf_of_bytes) {
-    if (n != s->n) return fail(CBGPU_ERR_INVALID, "LengthMismatch: n=%lld, session has %lld",
-                               (long long)n, (long long)s->n);
-    // sample validation (session.rs:2405-2428)
-    if (sample_len != 0) {
-        if (!s->sample_from_host)
-            return fail(CBGPU_ERR_INVALID,
-                        "Degenerate: a %lld-element host bootstrap sample was passed to a session opened "
-                        "with sample_from_host = false", (long long)sample_len);
-        if (sample_len != s->n)
-            return fail(CBGPU_ERR_INVALID, "LengthMismatch: sample has %lld elements, expected %lld",
-                        (long long)sample_len, (long long)s->n);
-        if (!sample) return fail(CBGPU_ERR_INVALID, "null sample pointer");
-    } else if (s->sample_from_host) {
-        return fail(CBGPU_ERR_INVALID,
-                    "Degenerate: the session was opened with sample_from_host = true but no sample "
-                    "was passed");
-    }
-    if (!s->target_ready && !target_h) return fail(CBGPU_ERR_INVALID, "target required on the first grow");
-    if (leaf_of && leaf_of_bytes) {
-        if (leaf_of_bytes != 1 && leaf_of_bytes != 2 && leaf_of_bytes != 4)
-            return fail(CBGPU_ERR_INVALID, "leaf_of_bytes must be 1, 2 or 4");
-        if (leaf_of_bytes == 1 && s->depth > 8) return fail(CBGPU_ERR_INVALID, "u8 leaf ids need depth <= 8");
-    }
-    CU(cudaSetDevice(s->device));
+// The device work of one tree, in stream order on s->st: everything from the
+// tree-state reset to the copies of the result into pinned host buffers.  It
+// makes no host decisions and no allocations, so it can be captured into a
+// graph once and replayed: per-tree scalars come from s->d_tp.
+// boot_mode: 0 none, 1 Bayesian, 2 Bernoulli; s_mode as launch_der.
+int enqueue_tree(cbgpu_session* s, int set, bool prof, int boot_mode, int s_mode, bool mvs, bool capturing,
+                 int* launches_out) {
     cudaStream_t st = s->st;
     const int D = s->depth;
     const int L = 1 << D;
-    const bool prof = s->profiling;
     int launches = 0;
     // event slots: 0 tree start, 1 after derivatives, per level l: 2+5l .. 6+5l, last: 2+5D
-    const int set = s->ev_set ^ 1;  // the other set may still hold the previous tree's unread times
-    auto rec = [&](int k) { if (prof || k == 0 || k == 2 + 5 * D) cudaEventRecord(s->ev[set][k], st); };
-
+    // (under capture they become event-record nodes; the External flag is only
+    // valid while capturing)
+    auto rec = [&](int k) {
+        if (!(prof || k == 0 || k == 2 + 5 * D)) return;
+        if (capturing) cudaEventRecordWithFlags(s->ev[set][k], st, cudaEventRecordExternal);
+        else cudaEventRecord(s->ev[set][k], st);
+    };
     rec(0);
-    if (!s->target_ready) {
-        CU(cudaMemcpyAsync(s->target, target_h, sizeof(double) * s->n, cudaMemcpyHostToDevice, st));
-        s->target_ready = true;
-    }
-    if (approx_h) {
-        CU(cudaMemcpyAsync(s->approx, approx_h, sizeof(double) * s->n, cudaMemcpyHostToDevice, st));
-        s->pending = false;
-    }
     CU(cudaMemsetAsync(s->ts, 0, sizeof(TreeState), st));
-
-    // ---- bootstrap: the host stream replica decides the draws (boosting.rs:6568-6660)
-    int s_mode = 0;
-    bool mvs = false;
-    uint64_t mvs_seed = 0;
-    double mvs_lam = 0.0;
-    if (s->sample_from_host) {
-        CU(cudaMemcpyAsync(s->sw64, sample, sizeof(double) * s->n, cudaMemcpyHostToDevice, st));
-        s_mode = 2;
-    } else if (s->boot != CBGPU_BOOT_NO) {
-        s->rng.gen();  // PRE_TREE_DRAWS = 2 (boosting.rs:59)
-        s->rng.gen();
-        if (s->boot == CBGPU_BOOT_BAYESIAN) {
-            if (s->temp != 0.0f) {
-                uint64_t rand_seed = s->rng.gen();
-                launch_bootstrap(1, s->n, s->row_offset, rand_seed, Rng64{}, 0.0, s->temp, s->sw32, st);
-                ++launches;
-                s_mode = 1;
-            }
-        } else if (s->boot == CBGPU_BOOT_BERNOULLI) {
-            if ((double)s->sample_rate < 1.0) {
-                Rng64 base = s->rng.r;
-                s->rng.advance((uint64_t)s->n_total);
-                launch_bootstrap(2, s->n, s->row_offset, 0, base, (double)s->sample_rate, 0.0f, s->sw32, st);
-                ++launches;
-                s_mode = 1;
-            }
-        } else if (s->boot == CBGPU_BOOT_MVS) {
-            if ((double)s->sample_rate < 1.0) {
-                if (s->has_mvs_lambda) mvs_lam = s->mvs_lambda;
-                else if (s->has_prev_mean) mvs_lam = s->prev_mean * s->prev_mean;
-                else {
-                    int rc = first_mvs_lambda(s, approx_h, target_h, &mvs_lam);
-                    if (rc) return rc;
-                }
-                mvs_seed = s->rng.gen();
-                mvs = true;
-                s_mode = 1;
-            }
-        }
+    if (boot_mode == 1) {
+        launch_bootstrap(1, s->n, s->row_offset, s->d_tp, 0.0, s->temp, s->sw32, st);
+        ++launches;
+    } else if (boot_mode == 2) {
+        launch_bootstrap(2, s->n, s->row_offset, s->d_tp, (double)s->sample_rate, 0.0f, s->sw32, st);
+        ++launches;
     }
-    launch_der(s->n, s->loss, s->approx, s->target, s->weight, s->leaf, s->pending ? s->leaf_lrv : nullptr,
-               s_mode, s->sw32, s->sw64, s->wd1, s->ts, mvs, st);
+    launch_der(s->n, s->loss, s->approx, s->target, s->weight, s->leaf, s->leaf_lrv, s->d_tp, s_mode, s->sw32,
+               s->sw64, s->wd1, s->ts, mvs, st);
     ++launches;
-    s->pending = false;
     if (mvs) {
-        launch_mvs(s->n, s->row_offset, s->wd1, mvs_lam, (double)s->sample_rate, mvs_seed, nullptr,
-                   s->mvs_thr, s->sw32, st);
+        launch_mvs(s->n, s->row_offset, s->wd1, s->d_tp, (double)s->sample_rate, s->mvs_thr, s->sw32, st);
         launch_max_gh(s->n, s->wd1, s->weight, s->sw32, s->ts, st);
         launches += 3;
     }
@@ -641,16 +618,148 @@ int grow(cbgpu_session* s, const double* approx_h, const double* target_h, int64
     launch_leaf_values(D, D, s->leaf_sums, s->l2, s->lr, s->ts, s->leaf_raw, s->leaf_lrv, st);
     ++launches;
     CU(cudaGetLastError());
-    CU(cudaMemcpyAsync(&s->h_ts, s->ts, sizeof(TreeState), cudaMemcpyDeviceToHost, st));
-    std::vector<double> raw((size_t)L);
-    CU(cudaMemcpyAsync(raw.data(), s->leaf_raw, sizeof(double) * L, cudaMemcpyDeviceToHost, st));
+    CU(cudaMemcpyAsync(s->h_ts, s->ts, sizeof(TreeState), cudaMemcpyDeviceToHost, st));
+    CU(cudaMemcpyAsync(s->h_raw, s->leaf_raw, sizeof(double) * L, cudaMemcpyDeviceToHost, st));
+    rec(2 + 5 * D);
+    *launches_out = launches;
+    return CBGPU_OK;
+}
+
+// The tree graph for event set `set` and this launch shape, captured from
+// enqueue_tree on first use (the stream's own work only: thread-local capture).
+int ensure_graph(cbgpu_session* s, int set, bool prof, int boot_mode, int s_mode, bool mvs) {
+    const int key = (prof ? 1 : 0) | (boot_mode << 1) | (s_mode << 3) | (mvs ? 1 << 5 : 0);
+    if (s->graph[set] && s->graph_key[set] == key) return CBGPU_OK;
+    if (s->graph[set]) {
+        cudaGraphExecDestroy(s->graph[set]);
+        s->graph[set] = nullptr;
+    }
+    cudaGraph_t g = nullptr;
+    CU(cudaStreamBeginCapture(s->st, cudaStreamCaptureModeThreadLocal));
+    int launches = 0;
+    const int rc = enqueue_tree(s, set, prof, boot_mode, s_mode, mvs, true, &launches);
+    const cudaError_t ce = cudaStreamEndCapture(s->st, &g);
+    if (rc != CBGPU_OK || ce != cudaSuccess) {
+        if (g) cudaGraphDestroy(g);
+        if (rc != CBGPU_OK) return rc;
+        return fail(CBGPU_ERR_CUDA, "tree graph capture failed: %s", cudaGetErrorString(ce));
+    }
+    const cudaError_t ie = cudaGraphInstantiate(&s->graph[set], g, 0);
+    cudaGraphDestroy(g);
+    if (ie != cudaSuccess) {
+        s->graph[set] = nullptr;
+        return fail(CBGPU_ERR_CUDA, "tree graph instantiation failed: %s", cudaGetErrorString(ie));
+    }
+    s->graph_key[set] = key;
+    s->graph_launches[set] = launches;
+    return CBGPU_OK;
+}
+
+int grow(cbgpu_session* s, const double* approx_h, const double* target_h, int64_t n,
+         const double* sample, int64_t sample_len, int32_t* split_feature, int32_t* split_bin,
+         int32_t* n_splits, double* leaf_values, void* leaf_of, int32_t leaf_of_bytes) {
+    if (n != s->n) return fail(CBGPU_ERR_INVALID, "LengthMismatch: n=%lld, session has %lld",
+                               (long long)n, (long long)s->n);
+    // sample validation (session.rs:2405-2428)
+    if (sample_len != 0) {
+        if (!s->sample_from_host)
+            return fail(CBGPU_ERR_INVALID,
+                        "Degenerate: a %lld-element host bootstrap sample was passed to a session opened "
+                        "with sample_from_host = false", (long long)sample_len);
+        if (sample_len != s->n)
+            return fail(CBGPU_ERR_INVALID, "LengthMismatch: sample has %lld elements, expected %lld",
+                        (long long)sample_len, (long long)s->n);
+        if (!sample) return fail(CBGPU_ERR_INVALID, "null sample pointer");
+    } else if (s->sample_from_host) {
+        return fail(CBGPU_ERR_INVALID,
+                    "Degenerate: the session was opened with sample_from_host = true but no sample "
+                    "was passed");
+    }
+    if (!s->target_ready && !target_h) return fail(CBGPU_ERR_INVALID, "target required on the first grow");
+    if (leaf_of && leaf_of_bytes) {
+        if (leaf_of_bytes != 1 && leaf_of_bytes != 2 && leaf_of_bytes != 4)
+            return fail(CBGPU_ERR_INVALID, "leaf_of_bytes must be 1, 2 or 4");
+        if (leaf_of_bytes == 1 && s->depth > 8) return fail(CBGPU_ERR_INVALID, "u8 leaf ids need depth <= 8");
+    }
+    CU(cudaSetDevice(s->device));
+    cudaStream_t st = s->st;
+    const int D = s->depth;
+    const int L = 1 << D;
+    const bool prof = s->profiling;
+    const int set = s->ev_set ^ 1;  // the other set may still hold the previous tree's unread times
+
+    if (!s->target_ready) {
+        CU(cudaMemcpyAsync(s->target, target_h, sizeof(double) * s->n, cudaMemcpyHostToDevice, st));
+        s->target_ready = true;
+    }
+    if (approx_h) {
+        CU(cudaMemcpyAsync(s->approx, approx_h, sizeof(double) * s->n, cudaMemcpyHostToDevice, st));
+        s->pending = false;
+    }
+
+    // ---- bootstrap: the host stream replica decides the draws (boosting.rs:6568-6660)
+    TreeParams& tp = *s->h_tp;  // pinned; the previous tree's copy finished at its sync
+    tp = TreeParams{};
+    int s_mode = 0, boot_mode = 0;
+    bool mvs = false;
+    if (s->sample_from_host) {
+        CU(cudaMemcpyAsync(s->sw64, sample, sizeof(double) * s->n, cudaMemcpyHostToDevice, st));
+        s_mode = 2;
+    } else if (s->boot != CBGPU_BOOT_NO) {
+        s->rng.gen();  // PRE_TREE_DRAWS = 2 (boosting.rs:59)
+        s->rng.gen();
+        if (s->boot == CBGPU_BOOT_BAYESIAN) {
+            if (s->temp != 0.0f) {
+                tp.boot_seed = s->rng.gen();
+                boot_mode = 1;
+                s_mode = 1;
+            }
+        } else if (s->boot == CBGPU_BOOT_BERNOULLI) {
+            if ((double)s->sample_rate < 1.0) {
+                tp.boot_base = s->rng.r;
+                s->rng.advance((uint64_t)s->n_total);
+                boot_mode = 2;
+                s_mode = 1;
+            }
+        } else if (s->boot == CBGPU_BOOT_MVS) {
+            if ((double)s->sample_rate < 1.0) {
+                double lam = 0.0;
+                if (s->has_mvs_lambda) lam = s->mvs_lambda;
+                else if (s->has_prev_mean) lam = s->prev_mean * s->prev_mean;
+                else {
+                    int rc = first_mvs_lambda(s, approx_h, target_h, &lam);
+                    if (rc) return rc;
+                }
+                tp.mvs_lambda = lam;
+                tp.boot_seed = s->rng.gen();
+                mvs = true;
+                s_mode = 1;
+            }
+        }
+    }
+    tp.pending = s->pending ? 1 : 0;
+    CU(cudaMemcpyAsync(s->d_tp, s->h_tp, sizeof(TreeParams), cudaMemcpyHostToDevice, st));
+    s->pending = false;
+
+    // The first tree of a session is enqueued directly (it also sets the
+    // kernels' launch attributes); later trees replay one captured graph of
+    // the same work, so a tree costs one launch instead of ~90.
+    int launches = 0;
+    if (s->use_graphs && s->trees > 0) {
+        int rc = ensure_graph(s, set, prof, boot_mode, s_mode, mvs);
+        if (rc) return rc;
+        CU(cudaGraphLaunch(s->graph[set], st));
+        launches = s->graph_launches[set];
+    } else {
+        int rc = enqueue_tree(s, set, prof, boot_mode, s_mode, mvs, false, &launches);
+        if (rc) return rc;
+    }
     if (leaf_of && leaf_of_bytes) {
         if (!s->leaf_export) DA(*(uint32_t**)&s->leaf_export, s->n);
         launch_leaf_export(s->n, s->leaf, s->leaf_export, leaf_of_bytes, st);
         ++launches;
         CU(cudaMemcpyAsync(leaf_of, s->leaf_export, (size_t)leaf_of_bytes * s->n, cudaMemcpyDeviceToHost, st));
     }
-    rec(2 + 5 * D);
     // Host work that needs no device result runs while the tree executes: the
     // previous tree's event times, and the RNG phase after the tree
     // (boosting.rs:7267-7300 + device_draw_replay.rs), which depends only on
@@ -667,33 +776,34 @@ int grow(cbgpu_session* s, const double* approx_h, const double* target_h, int64
     }
     CU(cudaStreamSynchronize(st));
     CU(cudaGetLastError());
+    const TreeState& hts = *s->h_ts;
     s->ev_set = set;
     s->ev_pending[set] = true;
     s->ev_depth[set] = D;
     s->ev_prof[set] = prof;
     {
         double rows = 0;
-        for (int l = 0; l < D; ++l) rows += (double)s->h_ts.hist_rows[l];
+        for (int l = 0; l < D; ++l) rows += (double)hts.hist_rows[l];
         s->ev_host[set][0] = rows;
         s->ev_host[set][1] = (double)launches;
     }
-    if (s->h_ts.err) {
-        if (s->h_ts.err & kErrNoCandidate)
+    if (hts.err) {
+        if (hts.err & kErrNoCandidate)
             return fail(CBGPU_ERR_DEVICE, "Degenerate: no split candidate available");
-        return fail(CBGPU_ERR_DEVICE, "device error word 0x%x (non-finite derivative or range error)",
-                    s->h_ts.err);
+        return fail(CBGPU_ERR_DEVICE, "device error word 0x%x (non-finite derivative or range error)", hts.err);
     }
     for (int l = 0; l < D; ++l) {
-        if (split_feature) split_feature[l] = s->h_ts.split[l].feature;
-        if (split_bin) split_bin[l] = s->h_ts.split[l].bin;
+        if (split_feature) split_feature[l] = hts.split[l].feature;
+        if (split_bin) split_bin[l] = hts.split[l].bin;
     }
     if (n_splits) *n_splits = D;
-    if (leaf_values) memcpy(leaf_values, raw.data(), sizeof(double) * L);
+    const double* raw = s->h_raw;
+    if (leaf_values) memcpy(leaf_values, raw, sizeof(double) * L);
     s->pending = true;
     // last_iter_mean_leaf_value over the learning-rate-scaled leaves (bootstrap.rs:382-389)
     double acc = 0.0;
     for (int k = 0; k < L; ++k) {
-        double v = raw[(size_t)k] * s->lr;
+        double v = raw[k] * s->lr;
         acc += std::sqrt(v * v);
     }
     s->prev_mean = acc / (double)L;
@@ -901,6 +1011,12 @@ int cbgpu_session_set_profiling(cbgpu_session* s, int32_t enabled) {
     return CBGPU_OK;
 }
 
+int cbgpu_session_set_graphs(cbgpu_session* s, int32_t enabled) {
+    if (!s) return fail(CBGPU_ERR_INVALID, "null session");
+    s->use_graphs = enabled != 0;
+    return CBGPU_OK;
+}
+
 int cbgpu_session_rng_state(cbgpu_session* s, uint64_t* out5) {
     if (!s || !out5) return fail(CBGPU_ERR_INVALID, "bad arguments");
     out5[0] = s->rng.r.x1;
@@ -1040,20 +1156,31 @@ int cbgpu_bootstrap_weights(int32_t type, int64_t n, int64_t row_offset, uint64_
     DA(d_sw, n);
     double* d_der = nullptr;
     double* d_thr = nullptr;
+    TreeParams tp{};
+    tp.boot_seed = rand_seed;
+    tp.mvs_lambda = lambda;
+    if (rng_raw4) tp.boot_base = Rng64{rng_raw4[0], rng_raw4[1], rng_raw4[2], rng_raw4[3]};
+    TreeParams* d_tp;
+    DA(d_tp, 1);
+    CU(cudaMemcpy(d_tp, &tp, sizeof(tp), cudaMemcpyHostToDevice));
     if (type == CBGPU_BOOT_BAYESIAN) {
-        launch_bootstrap(1, n, row_offset, rand_seed, Rng64{}, 0.0, temp, d_sw, 0);
+        launch_bootstrap(1, n, row_offset, d_tp, 0.0, temp, d_sw, 0);
     } else if (type == CBGPU_BOOT_BERNOULLI) {
-        if (!rng_raw4) { cudaFree(d_sw); return fail(CBGPU_ERR_INVALID, "Bernoulli needs rng_raw4"); }
-        Rng64 base{rng_raw4[0], rng_raw4[1], rng_raw4[2], rng_raw4[3]};
-        launch_bootstrap(2, n, row_offset, 0, base, (double)sample_rate, 0.0f, d_sw, 0);
+        if (!rng_raw4) { cudaFree(d_sw); cudaFree(d_tp); return fail(CBGPU_ERR_INVALID, "Bernoulli needs rng_raw4"); }
+        launch_bootstrap(2, n, row_offset, d_tp, (double)sample_rate, 0.0f, d_sw, 0);
     } else if (type == CBGPU_BOOT_MVS) {
-        if (!der_obj || row_offset % 8192) { cudaFree(d_sw); return fail(CBGPU_ERR_INVALID, "MVS needs der_obj, aligned row_offset"); }
+        if (!der_obj || row_offset % 8192) {
+            cudaFree(d_sw);
+            cudaFree(d_tp);
+            return fail(CBGPU_ERR_INVALID, "MVS needs der_obj, aligned row_offset");
+        }
         DA(d_der, n);
         DA(d_thr, (n + 8191) / 8192);
         CU(cudaMemcpy(d_der, der_obj, sizeof(double) * n, cudaMemcpyHostToDevice));
-        launch_mvs(n, row_offset, d_der, lambda, (double)sample_rate, rand_seed, nullptr, d_thr, d_sw, 0);
+        launch_mvs(n, row_offset, d_der, d_tp, (double)sample_rate, d_thr, d_sw, 0);
     } else {
         cudaFree(d_sw);
+        cudaFree(d_tp);
         return fail(CBGPU_ERR_INVALID, "bootstrap type %d has no device weights", type);
     }
     CU(cudaGetLastError());
@@ -1061,6 +1188,7 @@ int cbgpu_bootstrap_weights(int32_t type, int64_t n, int64_t row_offset, uint64_
     CU(cudaMemcpy(h.data(), d_sw, sizeof(float) * n, cudaMemcpyDeviceToHost));
     for (int64_t i = 0; i < n; ++i) out[i] = (double)h[(size_t)i];
     cudaFree(d_sw);
+    cudaFree(d_tp);
     if (d_der) cudaFree(d_der);
     if (d_thr) cudaFree(d_thr);
     return CBGPU_OK;

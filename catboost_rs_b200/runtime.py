@@ -246,6 +246,10 @@ class B200Runtime:
     def set_profiling(self, on: bool) -> None:
         _lib.check(self._L.cbgpu_session_set_profiling(self._s, 1 if on else 0))
 
+    def set_graphs(self, on: bool) -> None:
+        """Replay each tree as one captured CUDA graph (default) or enqueue it."""
+        _lib.check(self._L.cbgpu_session_set_graphs(self._s, 1 if on else 0))
+
     def timing(self) -> np.ndarray:
         """[tree ms, hist ms, derive+score ms, partition ms, der+bootstrap ms,
         collectives ms, rows histogrammed, kernels launched] of the last tree."""

@@ -186,6 +186,12 @@ CBGPU_API int cbgpu_session_elapsed_ms(cbgpu_session* s, int32_t a, int32_t b, d
 /* Enable (1) / disable (0) per-stage CUDA-event timing (off by default). */
 CBGPU_API int cbgpu_session_set_profiling(cbgpu_session* s, int32_t enabled);
 
+/* From the second tree on, a session replays each tree's device work as one
+ * captured CUDA graph (on by default); 0 enqueues every kernel and collective
+ * of every tree instead.  Results are identical either way.  No counterpart
+ * in the reference. */
+CBGPU_API int cbgpu_session_set_graphs(cbgpu_session* s, int32_t enabled);
+
 /* Host TFastRng64 replica of the session's main stream (raw state + calls),
  * so a driver can check it stays in lockstep with cb-train's RNG. */
 CBGPU_API int cbgpu_session_rng_state(cbgpu_session* s, uint64_t* out5);
