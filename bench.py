@@ -117,16 +117,49 @@ def shard_bounds(n_total: int, world: int, rank: int):
 # ---------------------------------------------------------------------------
 
 class ClockSampler:
+    """SM clock and clock-event reasons sampled during the timed region: NVML
+    read-only queries every 10 ms (so even a short region gets samples), else
+    nvidia-smi's 50 ms loop.  Rows: [index, sm MHz, max sm MHz, power W,
+    active, hw_slowdown, hw_thermal_slowdown, sw_thermal_slowdown, sw_power_cap]."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, gpu: int):
-        self.gpu = gpu
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+        ids = [x.strip() for x in vis.split(",") if x.strip()]
+        self.gpu = int(ids[gpu]) if gpu < len(ids) and ids[gpu].isdigit() else gpu
         self.rows = []
         self.proc = None
+        self.stop = threading.Event()
+        self.nvml = None
+
+    def _poll_nvml(self, nv, h):
+        bits = [nv.nvmlClocksEventReasonHwSlowdown, nv.nvmlClocksEventReasonHwThermalSlowdown,
+                nv.nvmlClocksEventReasonSwThermalSlowdown, nv.nvmlClocksEventReasonSwPowerCap]
+        mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        while not self.stop.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                rs = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                pw = nv.nvmlDeviceGetPowerUsage(h) / 1000.0
+                self.rows.append([str(self.gpu), str(sm), str(mx), f"{pw:.1f}", hex(rs)] +
+                                 ["Active" if rs & b else "Not Active" for b in bits])
+            except Exception:
+                pass
+            self.stop.wait(0.01)
 
     def __enter__(self):
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            h = nv.nvmlDeviceGetHandleByIndex(self.gpu)
+            self.nvml = nv
+            self.t = threading.Thread(target=self._poll_nvml, args=(nv, h), daemon=True)
+            self.t.start()
+            return self
+        except Exception:
+            self.nvml = None
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}",
                                           "--format=csv,noheader,nounits", "-lms", "50"],
@@ -142,6 +175,13 @@ class ClockSampler:
             self.rows.append([x.strip() for x in line.split(",")])
 
     def __exit__(self, *a):
+        if self.nvml:
+            self.stop.set()
+            self.t.join(timeout=2)
+            try:
+                self.nvml.nvmlShutdown()
+            except Exception:
+                pass
         if self.proc:
             self.proc.terminate()
             try:
