@@ -329,3 +329,33 @@ def test_timing_sum_matches_per_tree_timing():
     assert sums[0][6] == sums[1][6] == per_tree[:, 6].sum()
     assert sums[0][7] == sums[1][7]
     assert (sums[1][:6] >= 0).all() and sums[1][0] > 0 and sums[1][1] > 0
+
+
+@pytest.mark.parametrize("boot", ["Bayesian", "Bernoulli", "MVS"])
+def test_tree_graphs_match_direct_enqueue(boot):
+    """Trees after the first replay one captured graph; enqueueing every tree
+    directly must give bit-identical trees and approximants, also when the
+    graph is re-captured (profiling switched on mid-fit)."""
+    X, y, borders = make_dataset(30000, 16, seed=11, nan_frac=0.05, border_count=48, loss="Logloss")
+    nb = max(len(b) for b in borders) + 1
+    runs = []
+    for graphs in (True, False):
+        rt = cb.B200Runtime()
+        cfg = cb.DeviceTrainConfig(bootstrap_type=boot, sample_rate=0.7, rng_seed=9)
+        assert rt.begin_device_training_raw("Logloss", 6, True, 1, "Cosine", _cols(X), borders, None, X.shape[0],
+                                            X.shape[1], nb, 0.1, 3.0, cfg)
+        rt.set_graphs(graphs)
+        trees = []
+        for it in range(5):
+            if it == 3:
+                rt.set_profiling(True)
+            t = rt.grow_tree_on_device(None, y, [], leaf_of_bytes=2, resident_approx=True)
+            trees.append((t.splits, t.leaf_values.copy(), t.leaf_of.copy()))
+        runs.append((trees, rt.resident_approx()))
+        rt.end_device_training()
+    (ta, aa), (tb, ab) = runs
+    for (sa, la, oa), (sb, lb, ob) in zip(ta, tb):
+        assert sa == sb
+        np.testing.assert_array_equal(la, lb)
+        np.testing.assert_array_equal(oa, ob)
+    np.testing.assert_array_equal(aa, ab)
