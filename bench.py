@@ -134,31 +134,39 @@ class ClockSampler:
         self.stop = threading.Event()
         self.nvml = None
 
-    def _poll_nvml(self, nv, h):
+    def _sample_nvml(self, nv, h, mx):
         bits = [nv.nvmlClocksEventReasonHwSlowdown, nv.nvmlClocksEventReasonHwThermalSlowdown,
                 nv.nvmlClocksEventReasonSwThermalSlowdown, nv.nvmlClocksEventReasonSwPowerCap]
-        mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
-        while not self.stop.is_set():
+        sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+        rs = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+        try:
+            pw = nv.nvmlDeviceGetPowerUsage(h) / 1000.0
+        except Exception:
+            pw = float("nan")
+        self.rows.append([str(self.gpu), str(sm), str(mx), f"{pw:.1f}", hex(rs)] +
+                         ["Active" if rs & b else "Not Active" for b in bits])
+
+    def _poll_nvml(self):
+        while not self.stop.wait(0.01):
             try:
-                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
-                rs = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
-                pw = nv.nvmlDeviceGetPowerUsage(h) / 1000.0
-                self.rows.append([str(self.gpu), str(sm), str(mx), f"{pw:.1f}", hex(rs)] +
-                                 ["Active" if rs & b else "Not Active" for b in bits])
-            except Exception:
-                pass
-            self.stop.wait(0.01)
+                self._sample_nvml(self.nvml, self.h, self.mx)
+            except Exception as e:
+                self.error = repr(e)
 
     def __enter__(self):
+        self.error = None
         try:
             import pynvml as nv
             nv.nvmlInit()
-            h = nv.nvmlDeviceGetHandleByIndex(self.gpu)
+            self.h = nv.nvmlDeviceGetHandleByIndex(self.gpu)
+            self.mx = nv.nvmlDeviceGetMaxClockInfo(self.h, nv.NVML_CLOCK_SM)
             self.nvml = nv
-            self.t = threading.Thread(target=self._poll_nvml, args=(nv, h), daemon=True)
+            self._sample_nvml(nv, self.h, self.mx)  # the region's first sample, taken synchronously
+            self.t = threading.Thread(target=self._poll_nvml, daemon=True)
             self.t.start()
             return self
-        except Exception:
+        except Exception as e:
+            self.error = repr(e)
             self.nvml = None
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}",
@@ -179,9 +187,10 @@ class ClockSampler:
             self.stop.set()
             self.t.join(timeout=2)
             try:
+                self._sample_nvml(self.nvml, self.h, self.mx)  # and its last
                 self.nvml.nvmlShutdown()
-            except Exception:
-                pass
+            except Exception as e:
+                self.error = repr(e)
         if self.proc:
             self.proc.terminate()
             try:
@@ -191,7 +200,10 @@ class ClockSampler:
 
     def summary(self):
         if not self.rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+            out = {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+            if self.error:
+                out["error"] = self.error
+            return out
         sm = [float(r[1]) for r in self.rows if len(r) > 2 and r[1].replace(".", "").isdigit()]
         mx = [float(r[2]) for r in self.rows if len(r) > 2 and r[2].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
@@ -201,7 +213,8 @@ class ClockSampler:
                 if len(r) > 5 + k and r[5 + k].lower().startswith("active"):
                     reasons.add(nm)
         return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(self.rows)}
+                "reasons": sorted(reasons), "samples": len(self.rows),
+                "source": "nvml" if self.nvml else "nvidia-smi"}
 
 
 # ---------------------------------------------------------------------------
