@@ -52,6 +52,30 @@ double orc_sum_f64(const double* v, int64_t n);
 void orc_quantize(const float* cols, int64_t n, int32_t F, const double* borders_flat,
                   const int32_t* border_counts, uint8_t* out_bins_fm);
 
+/* ---- border selection (crates/cb-data/src/borders.rs, border_types.rs) - */
+/* EBorderSelectionType in the reference's listing order (border_types.rs:112-124). */
+enum {
+    ORC_BORDER_MEDIAN = 0, ORC_BORDER_GREEDY_LOGSUM = 1, ORC_BORDER_UNIFORM_AND_QUANTILES = 2,
+    ORC_BORDER_MIN_ENTROPY = 3, ORC_BORDER_MAX_LOGSUM = 4, ORC_BORDER_UNIFORM = 5,
+    ORC_BORDER_GREEDY_MIN_ENTROPY = 6
+};
+enum { ORC_PENALTY_MAXSUMLOG = 0, ORC_PENALTY_MIN_ENTROPY = 1 };
+enum { ORC_NAN_MIN = 0, ORC_NAN_MAX = 1, ORC_NAN_FORBIDDEN = 2 };
+
+/* Borders of one f32 column as catboost-rs's builder derives them
+ * (builder.rs:1677-1720 -> select_borders_f32, border_types.rs:134-236):
+ * columns over 200,000 rows use the fixed-seed 200k object sample, NaNs are
+ * dropped, a NaN-bearing column spends one border on the nan_mode sentinel
+ * (f32::MIN prepended under Min, f32::MAX appended under Max).  Returns the
+ * number of borders written (ascending f64), or < 0 on error.  MaxLogSum and
+ * MinEntropy (the exact DP binarizers) return -2. */
+int64_t orc_select_borders(const float* col, int64_t n, int32_t border_count, int32_t border_type,
+                           int32_t nan_mode, double* out, int64_t out_cap);
+
+/* sample_indices_for_build_borders (borders.rs:504-520): the sorted object
+ * sample (malloc'd; the caller frees it). */
+int64_t* orc_border_sample_indices(int64_t n, int64_t sample_size, int64_t* out_len);
+
 /* ---- derivatives (crates/cb-compute/src/loss.rs:35-80) ----------------- */
 enum { ORC_LOSS_RMSE = 0, ORC_LOSS_LOGLOSS = 1, ORC_LOSS_CROSSENTROPY = 2 };
 void orc_compute_gradients(int32_t loss, const double* approx, const double* target, int64_t n,

@@ -20,6 +20,9 @@ _lib = None
 LOSS = {"RMSE": 0, "Logloss": 1, "CrossEntropy": 2}
 BOOT = {"No": 0, "Bayesian": 1, "Bernoulli": 2, "MVS": 3}
 SCORE = {"Cosine": 0, "L2": 1}
+BORDER_TYPE = {"Median": 0, "GreedyLogSum": 1, "UniformAndQuantiles": 2, "MinEntropy": 3,
+               "MaxLogSum": 4, "Uniform": 5, "GreedyMinEntropy": 6}
+NAN_MODE = {"Min": 0, "Max": 1, "Forbidden": 2}
 
 
 def build() -> str:
@@ -84,6 +87,11 @@ def lib():
         L.orc_bootstrap.restype = C.c_int
         L.orc_build_histogram.argtypes = [C.c_void_p, C.c_int64, C.c_int32, C.c_int32, C.c_void_p,
                                           C.c_void_p, C.c_void_p, C.c_int32, C.c_void_p]
+        L.orc_select_borders.argtypes = [C.c_void_p, C.c_int64, C.c_int32, C.c_int32, C.c_int32,
+                                         C.c_void_p, C.c_int64]
+        L.orc_select_borders.restype = C.c_int64
+        L.orc_border_sample_indices.argtypes = [C.c_int64, C.c_int64, P(C.c_int64)]
+        L.orc_border_sample_indices.restype = C.c_void_p
         L.orc_train.argtypes = [P(_TrainArgs), P(_TrainOut)]
         L.orc_train.restype = C.c_int
         _lib = L
@@ -157,6 +165,30 @@ def quantize(cols_fm: np.ndarray, borders) -> np.ndarray:
     out = np.empty((F, n), dtype=np.uint8)
     lib().orc_quantize(_p(cols), n, F, _p(flat), _p(counts), _p(out))
     return out
+
+
+def select_borders(column, border_count: int, border_type: str = "GreedyLogSum",
+                   nan_mode: str = "Min") -> np.ndarray:
+    """Borders of one f32 column as the reference's builder derives them
+    (builder.rs:1677-1720, border_types.rs:134-236); ascending f64."""
+    col = np.ascontiguousarray(column, dtype=np.float32)
+    out = np.empty(int(border_count) + 2, dtype=np.float64)
+    k = lib().orc_select_borders(_p(col), col.size, int(border_count), BORDER_TYPE[border_type],
+                                 NAN_MODE[nan_mode], _p(out), out.size)
+    if k < 0:
+        raise ValueError(f"select_borders({border_type}, nan_mode={nan_mode}) failed: {k}")
+    return out[:k].copy()
+
+
+def border_sample_indices(n: int, sample_size: int = 200_000) -> np.ndarray:
+    """The fixed-seed sorted object sample of borders.rs:504-520."""
+    m = C.c_int64(0)
+    ptr = lib().orc_border_sample_indices(n, sample_size, C.byref(m))
+    if not ptr:
+        raise MemoryError("orc_border_sample_indices")
+    arr = np.ctypeslib.as_array(C.cast(ptr, C.POINTER(C.c_int64)), shape=(m.value,)).copy()
+    C.CDLL(None).free(C.c_void_p(ptr))
+    return arr
 
 
 def compute_gradients(loss: str, approx, target):

@@ -170,18 +170,51 @@ def e2e_fixtures(ref):
     return written
 
 
+def border_fixtures(ref):
+    """Standalone upstream border sets (Pool.quantize().save_quantization_borders())
+    from the reference's border_types/ and borders_quant/ fixtures, with the input
+    columns narrowed to f32 (the reference narrows with `v as f32` before selecting)."""
+    fx = os.path.join(ref, "crates/cb-oracle/fixtures")
+    inputs = {
+        "borders_dense": "inputs/borders_dense/X.npy",
+        "borders_runs": "inputs/borders_runs/X.npy",
+        "numeric_nan": "inputs/numeric_nan/X.npy",
+        "numeric_tiny": "inputs/numeric_tiny/X.npy",
+        "float_only_byte_identity": "float_only_byte_identity/inputs/X.npy",
+    }
+    arrays = {f"X__{k}": np.load(os.path.join(fx, v)).astype(np.float32) for k, v in inputs.items()}
+    cells = []
+    cfg = json.loads(_read(os.path.join(fx, "border_types/config.json")))
+    for stem, sc in sorted(cfg["scenarios"].items()):
+        cells.append({"stem": stem, "dataset": sc["dataset"], "border_count": int(sc["border_count"]),
+                      "border_type": sc["feature_border_type"], "nan_mode": sc["nan_mode"]})
+        arrays[f"B__{stem}"] = np.load(os.path.join(fx, "border_types", f"{stem}.borders.npy"))
+        arrays[f"C__{stem}"] = np.load(os.path.join(fx, "border_types", f"{stem}.borders_per_feature.npy"))
+    qcfg = json.loads(_read(os.path.join(fx, "borders_quant/config.json")))
+    for ds, sc in sorted(qcfg["scenarios"].items()):
+        stem = f"quant.{ds}"
+        cells.append({"stem": stem, "dataset": sc["input_dataset"], "border_count": int(sc["border_count"]),
+                      "border_type": sc["border_selection_type"], "nan_mode": sc["nan_mode"]})
+        arrays[f"B__{stem}"] = np.load(os.path.join(fx, "borders_quant", f"{ds}.borders.npy"))
+        arrays[f"C__{stem}"] = np.load(os.path.join(fx, "borders_quant", f"{ds}.borders_per_feature.npy"))
+    arrays["cells"] = np.array(json.dumps(cells))
+    np.savez_compressed(os.path.join(OUT, "borders.npz"), **arrays)
+    return [c["stem"] for c in cells]
+
+
 def main():
     ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("CB_REFERENCE", "")
     if not ref or not os.path.isdir(ref):
         sys.exit("usage: make_golden.py <reference checkout>")
     with open(os.path.join(OUT, "scalar_vectors.json"), "w") as f:
         json.dump(scalar_vectors(ref), f, indent=1)
+    border_cells = border_fixtures(ref)
     written = e2e_fixtures(ref)
     with open(os.path.join(OUT, "MANIFEST.json"), "w") as f:
         json.dump({"generator": "tests/golden/make_golden.py",
                    "origin": "upstream CatBoost 1.2.10 fixtures committed under the reference's "
                              "crates/cb-oracle/fixtures (thread_count=1, random_strength per scenario)",
-                   "scenarios": written}, f, indent=1)
+                   "scenarios": written, "border_cells": border_cells}, f, indent=1)
     print("wrote", len(written), "scenarios")
 
 
