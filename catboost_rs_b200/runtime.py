@@ -22,6 +22,9 @@ LOSS = {"RMSE": 0, "Rmse": 0, "Logloss": 1, "CrossEntropy": 2}
 SCORE = {"Cosine": 0, "L2": 1, "SolarL2": 2, "NewtonL2": 3, "NewtonCosine": 4, "LOOL2": 5, "SatL2": 6}
 BOOT = {"No": 0, "Bayesian": 1, "Bernoulli": 2, "MVS": 3, "Mvs": 3, "Poisson": 4}
 GROW = {"SymmetricTree": 0, "Depthwise": 1, "Lossguide": 2, "Region": 3}
+BORDER_TYPE = {"Median": 0, "GreedyLogSum": 1, "UniformAndQuantiles": 2, "MinEntropy": 3,
+               "MaxLogSum": 4, "Uniform": 5, "GreedyMinEntropy": 6}
+NAN_MODE = {"Min": 0, "Max": 1, "Forbidden": 2}
 
 
 @dataclass
@@ -292,6 +295,32 @@ def histogram(bins_row_major, g, h, leaf_of=None, n_leaves=1, n_bins=None) -> np
     out = np.empty((n_leaves, F, B, 2), dtype=np.float64)
     _lib.check(L.cbgpu_histogram(_ptr(bins), n, F, B, _ptr(g), _ptr(h), _ptr(lo), n_leaves, _ptr(out)))
     return out
+
+
+def select_borders(columns, border_count: int = 254, border_type: str = "GreedyLogSum",
+                   nan_mode: str = "Min", device: int = 0):
+    """Device border selection for every float column, as catboost-rs's builder
+    derives them (builder.rs:1677-1720 -> cb_data::select_borders_f32).
+
+    Returns one ascending f64 array per column, or None when the border type
+    is one the device declines (the exact MinEntropy / MaxLogSum binarizers).
+    """
+    L = _lib.load()
+    cols = [np.ascontiguousarray(c, dtype=np.float32) for c in columns]
+    if not cols:
+        raise ValueError("select_borders: no columns")
+    n = cols[0].size
+    if any(c.size != n for c in cols):
+        raise ValueError("select_borders: columns differ in length")
+    F = len(cols)
+    ptrs = (C.c_void_p * F)(*[c.ctypes.data for c in cols])
+    out = np.empty((F, max(int(border_count), 1)), dtype=np.float64)
+    counts = np.zeros(F, dtype=np.int32)
+    rc = L.cbgpu_select_borders(ptrs, n, F, int(border_count), BORDER_TYPE[border_type], NAN_MODE[nan_mode],
+                                device, _ptr(out), _ptr(counts))
+    if _lib.check(rc) == _lib.DECLINED:
+        return None
+    return [out[f, :counts[f]].copy() for f in range(F)]
 
 
 def bootstrap_weights(kind: str, n: int, *, row_offset=0, rand_seed=0, rng_raw4=None, sample_rate=1.0,

@@ -240,6 +240,39 @@ CBGPU_API int cbgpu_histogram_noalloc(const uint8_t* d_bins_row_major, int64_t n
                                       int32_t row_stride, int32_t n_bins, const double* d_g,
                                       const double* d_h, double* d_out_hist, void* stream);
 
+/* ---- fit preparation -------------------------------------------------- */
+
+/* EBorderSelectionType (crates/cb-data/src/border_types.rs:52-70), in the
+ * reference's listing order. */
+typedef enum {
+    CBGPU_BORDER_MEDIAN = 0, CBGPU_BORDER_GREEDY_LOGSUM = 1, CBGPU_BORDER_UNIFORM_AND_QUANTILES = 2,
+    CBGPU_BORDER_MIN_ENTROPY = 3, CBGPU_BORDER_MAX_LOGSUM = 4, CBGPU_BORDER_UNIFORM = 5,
+    CBGPU_BORDER_GREEDY_MIN_ENTROPY = 6
+} cbgpu_border_type;
+
+/* NanMode (crates/cb-data/src/nan_mode.rs). */
+typedef enum { CBGPU_NAN_MIN = 0, CBGPU_NAN_MAX = 1, CBGPU_NAN_FORBIDDEN = 2 } cbgpu_nan_mode;
+
+/* Quantization borders of every float column, selected on the device.
+ * Replaces the builder's per-column border derivation
+ * (crates/catboost-rs/src/builder.rs:1677-1720 -> cb_data::select_borders_f32,
+ * crates/cb-data/src/border_types.rs:134-236 and borders.rs:272-345): columns
+ * longer than 200,000 rows select from the reference's fixed-seed 200,000-row
+ * sample (borders.rs:504-520); NaNs are dropped; a column holding a NaN spends
+ * one of its border_count borders on the nan_mode sentinel (f32::MIN first
+ * under Min, f32::MAX last under Max); Forbidden with a NaN column returns
+ * CBGPU_ERR_INVALID with the builder's message.
+ *  float_columns[f]  host pointer to n f32 values of feature f;
+ *  border_count      1..1024 borders per feature, sentinel included;
+ *  border_type       GreedyLogSum (the default), GreedyMinEntropy, Median,
+ *                    Uniform or UniformAndQuantiles; the exact binarizers
+ *                    (MinEntropy, MaxLogSum) return CBGPU_DECLINED;
+ *  borders_out       [n_features][border_count] f64: feature f's ascending
+ *                    borders in its first counts_out[f] slots. */
+CBGPU_API int cbgpu_select_borders(const float* const* float_columns, int64_t n, int32_t n_features,
+                                   int32_t border_count, int32_t border_type, int32_t nan_mode,
+                                   int32_t device, double* borders_out, int32_t* counts_out);
+
 /* NCCL unique id (128 bytes) for world_size > 1 sessions. */
 CBGPU_API int cbgpu_nccl_unique_id(uint8_t* out128);
 
