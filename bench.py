@@ -27,6 +27,8 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 BLOCK_ROWS = 1 << 20       # data is generated in fixed 1Mi-row blocks so any sharding sees the same rows
+# cb-train hands the seam the learning rate narrowed to f32 (boosting.rs:4958)
+LR_SEAM = float(np.float32(0.05))
 BORDER_SAMPLE = 200_000    # fixed-seed sample the borders are selected from (cf. cb-data's 200k sample)
 FMIN = float(np.finfo(np.float32).min)
 # DRAM bytes (read + write) per histogrammed row, from an ncu capture of all
@@ -327,7 +329,7 @@ def main():
                                    world_size=world, row_offset=row_offset, n_total=args.rows,
                                    nccl_unique_id=uid)
         ok = rt.begin_device_training_raw("Logloss", args.depth, True, 1, "Cosine", cols, borders, None, n, F,
-                                          max(len(b) for b in borders) + 1, 0.05, 3.0, cfg)
+                                          max(len(b) for b in borders) + 1, LR_SEAM, 3.0, cfg)
         if not ok:
             raise RuntimeError(rt.decline_reason)
         return rt

@@ -7,7 +7,8 @@ include/cbgpu.h).  This package holds the host-side mirror of the reference's
 """
 from ._lib import CbGpuError, load as load_library  # noqa: F401
 from .runtime import (B200Runtime, DeviceGrownTree, DeviceTrainConfig, Derivatives,  # noqa: F401
-                      bootstrap_weights, histogram, nccl_unique_id, select_borders)
+                      apply_oblivious, bootstrap_weights, flatten_oblivious, histogram, nccl_unique_id,
+                      select_borders)
 from .boosting import FitParams, ObliviousModel, fit, seq_sum, starting_approx  # noqa: F401
 
 __version__ = "0.1.0"

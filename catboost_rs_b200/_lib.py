@@ -36,7 +36,7 @@ EXPORTS = [
     "cbgpu_session_timing", "cbgpu_session_timing_sum", "cbgpu_session_set_profiling", "cbgpu_session_set_graphs", "cbgpu_session_rng_state",
     "cbgpu_histogram", "cbgpu_bootstrap_weights", "cbgpu_nccl_unique_id", "cbgpu_version",
     "cbgpu_session_mark", "cbgpu_session_elapsed_ms", "cbgpu_histogram_noalloc",
-    "cbgpu_select_borders",
+    "cbgpu_select_borders", "cbgpu_apply_oblivious",
 ]
 
 _lib = None
@@ -80,6 +80,7 @@ def load(path: str = LIB_PATH):
         "cbgpu_bootstrap_weights": ([i32, i64, i64, u64, vp, f32, f32, vp, f64, vp], C.c_int),
         "cbgpu_histogram_noalloc": ([vp, i64, i32, i32, i32, vp, vp, vp, vp], C.c_int),
         "cbgpu_select_borders": ([vp, i64, i32, i32, i32, i32, i32, vp, vp], C.c_int),
+        "cbgpu_apply_oblivious": ([vp, i64, i32, vp, vp, vp, i32, vp, vp, f64, vp, i32, vp], C.c_int),
         "cbgpu_nccl_unique_id": ([vp], C.c_int),
         "cbgpu_version": ([], C.c_char_p),
     }

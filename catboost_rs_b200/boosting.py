@@ -14,7 +14,7 @@ from typing import Optional, Sequence
 
 import numpy as np
 
-from .runtime import B200Runtime, DeviceTrainConfig
+from .runtime import B200Runtime, DeviceTrainConfig, apply_oblivious, flatten_oblivious
 
 
 @dataclass
@@ -48,22 +48,15 @@ class ObliviousModel:
         return np.array([[self.borders[f][b] for f, b in zip(rf, rb)]
                          for rf, rb in zip(self.split_feature, self.split_bin)])
 
-    def predict(self, X) -> np.ndarray:
-        """Raw approximant for rows of X (f32 [n, F]); float value > border passes,
-        NaN passes only on nan_mode=Max features (border list ends with f32::MAX)."""
+    def predict(self, X, device: int = 0) -> np.ndarray:
+        """Raw approximant for rows of X (f32 [n, F]) through the device apply
+        (Model::predict_raw_on_device): float value > border passes, NaN passes
+        only on nan_mode=Max features (border list ends with f32::MAX)."""
         X = np.asarray(X, dtype=np.float32)
-        out = np.full(X.shape[0], self.bias, dtype=np.float64)
         fmax = np.float64(np.finfo(np.float32).max)
-        for t in range(self.split_feature.shape[0]):
-            leaf = np.zeros(X.shape[0], dtype=np.int64)
-            for l in range(self.split_feature.shape[1]):
-                f = int(self.split_feature[t, l])
-                b = self.borders[f][int(self.split_bin[t, l])]
-                v = X[:, f].astype(np.float64)
-                nan_max = len(self.borders[f]) > 0 and self.borders[f][-1] == fmax
-                leaf |= (((v > b) | (np.isnan(v) & nan_max)).astype(np.int64)) << l
-            out += self.leaf_values[t][leaf]
-        return out
+        nan_above = np.array([len(b) > 0 and b[-1] == fmax for b in self.borders], dtype=np.uint8)
+        flat = flatten_oblivious(self.split_feature, self.split_borders(), self.leaf_values)
+        return apply_oblivious(np.ascontiguousarray(X.T), flat, self.bias, nan_above, device)
 
 
 def seq_sum(v) -> float:
@@ -108,6 +101,9 @@ def fit(float_columns: Sequence[np.ndarray], borders: Sequence[Sequence[float]],
         sw = float(n_total)
     scaled_l2 = p.l2_leaf_reg * (sw / n_total) if n_total else p.l2_leaf_reg
     b0 = bias if bias is not None else starting_approx(p, t)
+    # upstream stores the learning rate as f32, and cb-train hands the narrowed
+    # value to the seam and to normalize_leaf_values (boosting.rs:4958)
+    lr = float(np.float32(p.learning_rate))
     n_bins = max(len(b) for b in borders) + 1
     cfg = DeviceTrainConfig(bootstrap_type=p.bootstrap_type, sample_rate=p.subsample,
                             rng_seed=p.random_seed, bias=b0, sample_from_host=False,
@@ -117,7 +113,7 @@ def fit(float_columns: Sequence[np.ndarray], borders: Sequence[Sequence[float]],
                             nccl_unique_id=pl.get("nccl_unique_id"))
     rt = B200Runtime()
     ok = rt.begin_device_training_raw(p.loss, p.depth, True, 1, p.score_function, cols, borders, w,
-                                      n, F, n_bins, p.learning_rate, scaled_l2, cfg)
+                                      n, F, n_bins, lr, scaled_l2, cfg)
     if not ok:
         raise RuntimeError(f"device declined: {rt.decline_reason}")
     if profile:
@@ -133,7 +129,7 @@ def fit(float_columns: Sequence[np.ndarray], borders: Sequence[Sequence[float]],
             tree = rt.grow_tree_on_device(None, t, [], leaf_of_bytes=0, resident_approx=True)
             for l, (f, b, _) in enumerate(tree.splits):
                 sf[it, l], sb[it, l] = f, b
-            lv[it] = tree.leaf_values * p.learning_rate  # normalize_leaf_values
+            lv[it] = tree.leaf_values * lr  # normalize_leaf_values
             if staged:
                 st[it] = rt.resident_approx()
             if profile:

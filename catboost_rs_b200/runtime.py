@@ -323,6 +323,48 @@ def select_borders(columns, border_count: int = 254, border_type: str = "GreedyL
     return [out[f, :counts[f]].copy() for f in range(F)]
 
 
+def flatten_oblivious(split_feature, split_border, leaf_values):
+    """CSR lowering of an oblivious ensemble, cb_model::flatten_oblivious_f64
+    (crates/cb-model/src/gpu_apply.rs:120-193): split_feature [T, D] (-1 marks
+    an unused level), split_border [T, D] border values, leaf_values [T, 2^D]
+    learning-rate scaled (a tree with d splits owns its first 2^d values).
+    Returns (split_features, split_borders, tree_split_offsets, leaf_values,
+    tree_leaf_offsets)."""
+    sf = np.asarray(split_feature)
+    sb = np.asarray(split_border, dtype=np.float64)
+    lv = np.asarray(leaf_values, dtype=np.float64)
+    depth = (sf >= 0).sum(axis=1) if sf.size else np.zeros(sf.shape[0], dtype=np.int64)
+    keep = sf >= 0
+    so = np.concatenate([[0], np.cumsum(depth)]).astype(np.uint32)
+    lo = np.concatenate([[0], np.cumsum(1 << depth.astype(np.int64))]).astype(np.uint32)
+    leaves = np.concatenate([lv[t, : 1 << int(d)] for t, d in enumerate(depth)]) if sf.shape[0] else np.zeros(0)
+    return (np.ascontiguousarray(sf[keep], dtype=np.uint32), np.ascontiguousarray(sb[keep], dtype=np.float64), so,
+            np.ascontiguousarray(leaves, dtype=np.float64), lo)
+
+
+def apply_oblivious(features_fm, flat, bias: float = 0.0, nan_above=None, device: int = 0) -> np.ndarray:
+    """Raw predictions on the device (Model::predict_raw_on_device,
+    crates/catboost-rs/src/model.rs:360-384): features_fm f32 [F][n]."""
+    L = _lib.load()
+    x = np.ascontiguousarray(features_fm, dtype=np.float32)
+    if x.ndim != 2:
+        raise ValueError("apply_oblivious: features must be [n_features][n]")
+    F, n = x.shape
+    # named, contiguous, correctly typed arrays stay alive across the call
+    sf = np.ascontiguousarray(flat[0], dtype=np.uint32)
+    sb = np.ascontiguousarray(flat[1], dtype=np.float64)
+    so = np.ascontiguousarray(flat[2], dtype=np.uint32)
+    lv = np.ascontiguousarray(flat[3], dtype=np.float64)
+    lo = np.ascontiguousarray(flat[4], dtype=np.uint32)
+    na = None if nan_above is None else np.ascontiguousarray(nan_above, dtype=np.uint8)
+    if so.size < 1 or lo.size != so.size or sf.size != sb.size or (na is not None and na.size < F):
+        raise ValueError("apply_oblivious: inconsistent flat model")
+    out = np.empty(n, dtype=np.float64)
+    _lib.check(L.cbgpu_apply_oblivious(_ptr(x), n, F, _ptr(sf), _ptr(sb), _ptr(so), so.size - 1, _ptr(lv), _ptr(lo),
+                                       float(bias), _ptr(na), device, _ptr(out)))
+    return out
+
+
 def bootstrap_weights(kind: str, n: int, *, row_offset=0, rand_seed=0, rng_raw4=None, sample_rate=1.0,
                       bagging_temperature=1.0, der_obj=None, mvs_lambda=0.0) -> np.ndarray:
     """Device bootstrap weights (crates/cb-train/src/bootstrap.rs semantics)."""

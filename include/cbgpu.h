@@ -273,6 +273,31 @@ CBGPU_API int cbgpu_select_borders(const float* const* float_columns, int64_t n,
                                    int32_t border_count, int32_t border_type, int32_t nan_mode,
                                    int32_t device, double* borders_out, int32_t* counts_out);
 
+/* ---- apply ------------------------------------------------------------- */
+
+/* Raw predictions (RawFormulaVal) of a float-only oblivious ensemble on the
+ * device: replaces cb_backend::gpu_runtime::launch_apply_oblivious_f64, the
+ * launcher behind Model::predict_raw_on_device
+ * (crates/catboost-rs/src/model.rs:360-384), over the same CSR lowering
+ * (cb_model::flatten_oblivious_f64, crates/cb-model/src/gpu_apply.rs:83-193).
+ * Results equal the CPU apply (crates/cb-model/src/apply.rs:150-173, 374-410)
+ * bit for bit.
+ *  features_fm        host, feature-major f32 [n_features][n];
+ *  split_features/_borders  [tree_split_offsets[n_trees]] per split; split s of
+ *                     tree t is leaf bit s - tree_split_offsets[t] and passes
+ *                     iff (double)x > border; a feature >= n_features never
+ *                     passes; at most 16 splits per tree;
+ *  leaf_values        [tree_leaf_offsets[n_trees]] learning-rate scaled;
+ *  nan_above          [n_features] 1 where NaN passes every split (the
+ *                     nan_mode=Max rule: the feature's last border is
+ *                     f32::MAX), or NULL; otherwise NaN never passes;
+ *  out                [n] host, bias + the per-tree values in tree order. */
+CBGPU_API int cbgpu_apply_oblivious(const float* features_fm, int64_t n, int32_t n_features,
+                                    const uint32_t* split_features, const double* split_borders,
+                                    const uint32_t* tree_split_offsets, int32_t n_trees,
+                                    const double* leaf_values, const uint32_t* tree_leaf_offsets, double bias,
+                                    const uint8_t* nan_above, int32_t device, double* out);
+
 /* NCCL unique id (128 bytes) for world_size > 1 sessions. */
 CBGPU_API int cbgpu_nccl_unique_id(uint8_t* out128);
 

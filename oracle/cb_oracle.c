@@ -636,6 +636,9 @@ int orc_train(const orc_train_args* a, orc_train_out* o) {
     for (int64_t i = 0; i < n; ++i) w[i] = a->weights ? a->weights[i] : 1.0;
     double sum_w = orc_sum_f64(w, n);
     double scaled_l2 = n == 0 ? a->l2_leaf_reg : a->l2_leaf_reg * (sum_w / (double)n);
+    /* upstream stores the learning rate as f32: every use below sees the
+     * narrowed value (boosting.rs:4958) */
+    const double lr = (double)(float)a->learning_rate;
     double bias = 0.0;
     if (a->boost_from_average && a->loss == ORC_LOSS_RMSE && n > 0)
         bias = orc_sum_f64(a->target, n) / (double)n;
@@ -683,7 +686,7 @@ int orc_train(const orc_train_args* a, orc_train_out* o) {
             double acc = 0.0;
             for (int64_t i = 0; i < n; ++i) acc += wd1[i] * wd1[i];
             double dsdz = n == 0 ? 0.0 : sqrt(acc / (double)n);
-            double model_length = (double)it * a->learning_rate;
+            double model_length = (double)it * lr;
             double left = exp(log((double)n) - model_length);
             std_dev = a->random_strength * dsdz * (left / (1.0 + left));
         }
@@ -707,7 +710,7 @@ int orc_train(const orc_train_args* a, orc_train_out* o) {
         double* lv = o->leaf_values + (size_t)it * L;
         for (int32_t k = 0; k < L; ++k) lv[k] = 0.0;
         for (int32_t k = 0; k < nl; ++k)
-            lv[k] = calc_average(ls[2 * k], ls[2 * k + 1], scaled_l2) * a->learning_rate;
+            lv[k] = calc_average(ls[2 * k], ls[2 * k + 1], scaled_l2) * lr;
         for (int64_t i = 0; i < n; ++i) approx[i] += lv[leaf[i]];
         if (o->staged) memcpy(o->staged + (size_t)it * n, approx, sizeof(double) * (size_t)n);
         if (draws) {

@@ -76,6 +76,19 @@ int64_t orc_select_borders(const float* col, int64_t n, int32_t border_count, in
  * sample (malloc'd; the caller frees it). */
 int64_t* orc_border_sample_indices(int64_t n, int64_t sample_size, int64_t* out_len);
 
+/* ---- apply (crates/cb-model/src/apply.rs:150-173, 264-271, 374-410) ---- */
+/* Raw prediction of a float-only oblivious ensemble in the flat CSR layout of
+ * cb_model::flatten_oblivious_f64 (crates/cb-model/src/gpu_apply.rs:83-110):
+ * x_fm feature-major f32 [F][n]; split s of tree t in [tree_split_offsets[t],
+ * tree_split_offsets[t+1]) is leaf bit s - tree_split_offsets[t] and passes iff
+ * (double)x > border (NaN: nan_above[f], the nan_mode=Max rule; a feature
+ * index >= F never passes); leaf_values already learning-rate scaled; the
+ * prediction is bias + the ordered sum over trees. */
+void orc_apply_oblivious(const float* x_fm, int64_t n, int32_t F, const uint32_t* split_features,
+                         const double* split_borders, const uint32_t* tree_split_offsets, int32_t n_trees,
+                         const double* leaf_values, const uint32_t* tree_leaf_offsets, double bias,
+                         const uint8_t* nan_above, double* out);
+
 /* ---- derivatives (crates/cb-compute/src/loss.rs:35-80) ----------------- */
 enum { ORC_LOSS_RMSE = 0, ORC_LOSS_LOGLOSS = 1, ORC_LOSS_CROSSENTROPY = 2 };
 void orc_compute_gradients(int32_t loss, const double* approx, const double* target, int64_t n,

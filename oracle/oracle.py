@@ -92,6 +92,9 @@ def lib():
         L.orc_select_borders.restype = C.c_int64
         L.orc_border_sample_indices.argtypes = [C.c_int64, C.c_int64, P(C.c_int64)]
         L.orc_border_sample_indices.restype = C.c_void_p
+        L.orc_apply_oblivious.argtypes = [C.c_void_p, C.c_int64, C.c_int32, C.c_void_p, C.c_void_p,
+                                          C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_double,
+                                          C.c_void_p, C.c_void_p]
         L.orc_train.argtypes = [P(_TrainArgs), P(_TrainOut)]
         L.orc_train.restype = C.c_int
         _lib = L
@@ -178,6 +181,38 @@ def select_borders(column, border_count: int, border_type: str = "GreedyLogSum",
     if k < 0:
         raise ValueError(f"select_borders({border_type}, nan_mode={nan_mode}) failed: {k}")
     return out[:k].copy()
+
+
+def flatten_oblivious(split_feature, split_border, leaf_values):
+    """CSR lowering of an oblivious ensemble (crates/cb-model/src/gpu_apply.rs:120-193):
+    split_feature [T, D] (-1 = no split at that level), split_border [T, D] border
+    values, leaf_values [T, 2^D] (learning-rate scaled; a tree with d splits uses
+    its first 2^d values)."""
+    sf = np.asarray(split_feature)
+    sb = np.asarray(split_border, dtype=np.float64)
+    lv = np.asarray(leaf_values, dtype=np.float64)
+    feats, bords, leaves, so, lo = [], [], [], [0], [0]
+    for t in range(sf.shape[0]):
+        d = int(np.sum(sf[t] >= 0))
+        feats.extend(int(f) for f in sf[t, :d])
+        bords.extend(float(b) for b in sb[t, :d])
+        leaves.extend(lv[t, : 1 << d])
+        so.append(len(feats))
+        lo.append(len(leaves))
+    return (np.array(feats, dtype=np.uint32), np.array(bords, dtype=np.float64), np.array(so, dtype=np.uint32),
+            np.array(leaves, dtype=np.float64), np.array(lo, dtype=np.uint32))
+
+
+def apply_oblivious(X_fm, flat, bias=0.0, nan_above=None) -> np.ndarray:
+    """Raw predictions of a flattened ensemble (crates/cb-model/src/apply.rs:374-410)."""
+    x = np.ascontiguousarray(X_fm, dtype=np.float32)
+    F, n = x.shape
+    feats, bords, so, leaves, lo = flat
+    na = None if nan_above is None else np.ascontiguousarray(nan_above, dtype=np.uint8)
+    out = np.empty(n, dtype=np.float64)
+    lib().orc_apply_oblivious(_p(x), n, F, _p(feats), _p(bords), _p(so), so.size - 1, _p(leaves), _p(lo),
+                              float(bias), _p(na), _p(out))
+    return out
 
 
 def border_sample_indices(n: int, sample_size: int = 200_000) -> np.ndarray:
