@@ -145,6 +145,42 @@ typedef struct {
 
 int orc_train(const orc_train_args* a, orc_train_out* o);
 
+/* ---- MultiClass (softmax) loop (boosting.rs multi-output CPU branch) --- */
+typedef struct {
+    int64_t n;
+    int32_t n_features;
+    const uint8_t* bins_fm;        /* [F][n] */
+    const int32_t* border_counts;  /* [F] */
+    const int32_t* target_class;   /* [n] class index in 0..n_classes-1 */
+    const double* weights;         /* [n] or NULL */
+    int32_t n_classes;             /* approx_dimension K */
+    int32_t depth;
+    int32_t iterations;
+    double learning_rate;
+    double l2_leaf_reg;
+    int32_t score_function;
+    int32_t bootstrap_type;
+    double subsample;
+    float bagging_temperature;
+    uint64_t random_seed;
+    int32_t n_threads;
+} orc_multi_args;
+
+typedef struct {
+    int32_t* split_feature;  /* [iterations * depth] */
+    int32_t* split_bin;      /* [iterations * depth] */
+    int32_t* tree_depth;     /* [iterations] */
+    double* leaf_values;     /* [iterations * 2^depth * K] LEAF-major, learning-rate scaled */
+    double* staged;          /* [iterations * n * K] object-major, or NULL */
+    double* final_approx;    /* [n * K] object-major, or NULL */
+} orc_multi_out;
+
+int orc_train_multiclass(const orc_multi_args* a, orc_multi_out* o);
+
+/* solve_symmetric_newton (crates/cb-compute/src/leaf.rs:281-340). */
+void orc_solve_symmetric_newton(const double* sum_der, const double* sum_der2_packed, int32_t k,
+                                double scaled_l2, double* out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -57,6 +57,22 @@ class _TrainOut(C.Structure):
                 ("bias", C.c_void_p), ("rng_calls", C.c_void_p)]
 
 
+class _MultiArgs(C.Structure):
+    _fields_ = [
+        ("n", C.c_int64), ("n_features", C.c_int32), ("bins_fm", C.c_void_p),
+        ("border_counts", C.c_void_p), ("target_class", C.c_void_p), ("weights", C.c_void_p),
+        ("n_classes", C.c_int32), ("depth", C.c_int32), ("iterations", C.c_int32),
+        ("learning_rate", C.c_double), ("l2_leaf_reg", C.c_double), ("score_function", C.c_int32),
+        ("bootstrap_type", C.c_int32), ("subsample", C.c_double), ("bagging_temperature", C.c_float),
+        ("random_seed", C.c_uint64), ("n_threads", C.c_int32),
+    ]
+
+
+class _MultiOut(C.Structure):
+    _fields_ = [("split_feature", C.c_void_p), ("split_bin", C.c_void_p), ("tree_depth", C.c_void_p),
+                ("leaf_values", C.c_void_p), ("staged", C.c_void_p), ("final_approx", C.c_void_p)]
+
+
 def lib():
     global _lib
     if _lib is None:
@@ -95,6 +111,9 @@ def lib():
         L.orc_apply_oblivious.argtypes = [C.c_void_p, C.c_int64, C.c_int32, C.c_void_p, C.c_void_p,
                                           C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_double,
                                           C.c_void_p, C.c_void_p]
+        L.orc_train_multiclass.argtypes = [P(_MultiArgs), P(_MultiOut)]
+        L.orc_train_multiclass.restype = C.c_int
+        L.orc_solve_symmetric_newton.argtypes = [C.c_void_p, C.c_void_p, C.c_int32, C.c_double, C.c_void_p]
         L.orc_train.argtypes = [P(_TrainArgs), P(_TrainOut)]
         L.orc_train.restype = C.c_int
         _lib = L
@@ -301,3 +320,49 @@ def train(bins_fm, border_counts, target, *, loss="RMSE", depth=6, iterations=10
     if rc != 0:
         raise RuntimeError(f"orc_train failed rc={rc}")
     return OracleFit(sf, sb, td, lv, st, fa, float(bias[0]), calls)
+
+
+@dataclass
+class OracleMultiFit:
+    split_feature: np.ndarray  # [iters, depth]
+    split_bin: np.ndarray      # [iters, depth]
+    tree_depth: np.ndarray     # [iters]
+    leaf_values: np.ndarray    # [iters, 2^depth, K] (leaf-major, learning-rate scaled)
+    staged: np.ndarray | None  # [iters, n, K]
+    final_approx: np.ndarray   # [n, K]
+
+
+def train_multiclass(bins_fm, border_counts, target_class, n_classes, *, depth=6, iterations=10,
+                     learning_rate=0.1, l2_leaf_reg=3.0, score_function="Cosine", bootstrap_type="No",
+                     subsample=0.66, bagging_temperature=1.0, random_seed=0, weights=None, staged=True,
+                     n_threads=0) -> OracleMultiFit:
+    """The reference's MultiClass (softmax, Newton leaves) CPU loop on quantized bins."""
+    bins = np.ascontiguousarray(bins_fm, dtype=np.uint8)
+    F, n = bins.shape
+    K = int(n_classes)
+    bc = np.ascontiguousarray(border_counts, dtype=np.int32)
+    y = np.ascontiguousarray(target_class, dtype=np.int32)
+    w = None if weights is None else np.ascontiguousarray(weights, dtype=np.float64)
+    L = 1 << depth
+    sf = np.empty((iterations, depth), dtype=np.int32)
+    sb = np.empty((iterations, depth), dtype=np.int32)
+    td = np.empty(iterations, dtype=np.int32)
+    lv = np.empty((iterations, L, K), dtype=np.float64)
+    st = np.empty((iterations, n, K), dtype=np.float64) if staged else None
+    fa = np.empty((n, K), dtype=np.float64)
+    args = _MultiArgs(n, F, _p(bins), _p(bc), _p(y), _p(w), K, depth, iterations, learning_rate, l2_leaf_reg,
+                      SCORE[score_function], BOOT[bootstrap_type], subsample, bagging_temperature, random_seed,
+                      n_threads)
+    out = _MultiOut(_p(sf), _p(sb), _p(td), _p(lv), _p(st), _p(fa))
+    rc = lib().orc_train_multiclass(C.byref(args), C.byref(out))
+    if rc != 0:
+        raise RuntimeError(f"orc_train_multiclass failed rc={rc}")
+    return OracleMultiFit(sf, sb, td, lv, st, fa)
+
+
+def solve_symmetric_newton(sum_der, sum_der2_packed, scaled_l2):
+    d = np.ascontiguousarray(sum_der, dtype=np.float64)
+    h = np.ascontiguousarray(sum_der2_packed, dtype=np.float64)
+    out = np.empty(d.size, dtype=np.float64)
+    lib().orc_solve_symmetric_newton(_p(d), _p(h), d.size, scaled_l2, _p(out))
+    return out

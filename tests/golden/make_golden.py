@@ -202,6 +202,37 @@ def border_fixtures(ref):
     return [c["stem"] for c in cells]
 
 
+def multiclass_fixture(ref):
+    """Upstream MultiClass (softmax, Newton leaves) fixture on numeric_tiny:
+    labels digitized at the 1/3 and 2/3 quantiles of y (the fixture's
+    target_rule), trees, LEAF-major leaf values, staged raw approximants and
+    class probabilities."""
+    fx = os.path.join(ref, "crates/cb-oracle/fixtures")
+    cfg = json.loads(_read(os.path.join(fx, "multiclass_softmax/config.json")))
+    model = json.loads(_read(os.path.join(fx, "multiclass_softmax/model.json")))
+    X = np.load(os.path.join(fx, "inputs/numeric_tiny/X.npy"))
+    y = np.load(os.path.join(fx, "inputs/numeric_tiny/y.npy"))
+    cls = np.digitize(y, np.quantile(y, [1 / 3, 2 / 3])).astype(np.int32)
+    K = int(cfg["approx_dimension"])
+    trees = model["oblivious_trees"]
+    depth = max(len(t["splits"]) for t in trees)
+    sf = np.array([[s["float_feature_index"] for s in t["splits"]] for t in trees], dtype=np.int32)
+    sv = np.array([[s["border"] for s in t["splits"]] for t in trees], dtype=np.float64)
+    lv = np.array([t["leaf_values"] for t in trees], dtype=np.float64).reshape(len(trees), 1 << depth, K)
+    n = X.shape[0]
+    p = cfg["params"]
+    params = {"loss": "MultiClass", "n_classes": K, "depth": int(p["depth"]), "iterations": int(p["iterations"]),
+              "learning_rate": float(p["learning_rate"]), "l2_leaf_reg": float(p["l2_leaf_reg"]),
+              "score_function": p["score_function"], "bootstrap_type": p["bootstrap_type"],
+              "random_seed": int(p["random_seed"]), "border_count": 254, "border_type": "GreedyLogSum"}
+    np.savez_compressed(os.path.join(OUT, "multiclass_softmax.npz"), X=X.astype(np.float32), target_class=cls,
+                        split_feature=sf, split_border=sv, leaf_values=lv,
+                        staged=np.load(os.path.join(fx, "multiclass_softmax/staged.npy")).reshape(len(trees), n, K),
+                        probabilities=np.load(os.path.join(fx, "multiclass_softmax/predictions.npy")).reshape(n, K),
+                        params=np.array(json.dumps(params)))
+    return "multiclass_softmax"
+
+
 def main():
     ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("CB_REFERENCE", "")
     if not ref or not os.path.isdir(ref):
@@ -210,6 +241,7 @@ def main():
         json.dump(scalar_vectors(ref), f, indent=1)
     border_cells = border_fixtures(ref)
     written = e2e_fixtures(ref)
+    written.append(multiclass_fixture(ref))
     with open(os.path.join(OUT, "MANIFEST.json"), "w") as f:
         json.dump({"generator": "tests/golden/make_golden.py",
                    "origin": "upstream CatBoost 1.2.10 fixtures committed under the reference's "
