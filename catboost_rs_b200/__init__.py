@@ -6,9 +6,10 @@ include/cbgpu.h).  This package holds the host-side mirror of the reference's
 (boosting.py) and the build script (build.py).
 """
 from ._lib import CbGpuError, load as load_library  # noqa: F401
-from .runtime import (B200Runtime, DeviceGrownTree, DeviceTrainConfig, Derivatives,  # noqa: F401
+from .runtime import (B200MultiRuntime, B200Runtime, DeviceGrownTree, DeviceTrainConfig, Derivatives,  # noqa: F401
                       apply_oblivious, bootstrap_weights, flatten_oblivious, histogram, nccl_unique_id,
                       select_borders)
-from .boosting import FitParams, ObliviousModel, fit, seq_sum, starting_approx  # noqa: F401
+from .boosting import (FitParams, MultiClassModel, ObliviousModel, fit, fit_multiclass,  # noqa: F401
+                       seq_sum, starting_approx)
 
 __version__ = "0.1.0"

@@ -14,7 +14,7 @@ from typing import Optional, Sequence
 
 import numpy as np
 
-from .runtime import B200Runtime, DeviceTrainConfig, apply_oblivious, flatten_oblivious
+from .runtime import B200MultiRuntime, B200Runtime, DeviceTrainConfig, apply_oblivious, flatten_oblivious
 
 
 @dataclass
@@ -137,3 +137,63 @@ def fit(float_columns: Sequence[np.ndarray], borders: Sequence[Sequence[float]],
     finally:
         rt.end_device_training()
     return ObliviousModel([np.asarray(b, dtype=np.float64) for b in borders], sf, sb, lv, b0, st, timings)
+
+
+@dataclass
+class MultiClassModel:
+    """Per-tree splits, the learning-rate scaled LEAF-major leaf blocks
+    [T, 2^depth, K], the borders, and optionally the staged raw approximants
+    [T, n, K] (object-major, upstream's staged_predict layout)."""
+    borders: list
+    split_feature: np.ndarray
+    split_bin: np.ndarray
+    leaf_values: np.ndarray
+    staged: Optional[np.ndarray] = None
+
+    def split_borders(self) -> np.ndarray:
+        return np.array([[self.borders[f][b] for f, b in zip(rf, rb)]
+                         for rf, rb in zip(self.split_feature, self.split_bin)])
+
+
+def fit_multiclass(float_columns: Sequence[np.ndarray], borders: Sequence[Sequence[float]], target_class,
+                   n_classes: int, params: FitParams, weights=None, *, staged: bool = False,
+                   device: int = 0) -> MultiClassModel:
+    """MultiClass (softmax, Newton leaves) fit on raw f32 columns with fixed
+    borders: cb-train's multi-output loop (boosting.rs:7400-8930 at
+    approx_dimension K) over the device's multi-output arm."""
+    p = params
+    cols = [np.ascontiguousarray(c, dtype=np.float32) for c in float_columns]
+    F = len(cols)
+    n = cols[0].size if F else 0
+    y = np.ascontiguousarray(target_class, dtype=np.float64)
+    w = None if weights is None else np.ascontiguousarray(weights, dtype=np.float64)
+    sw = seq_sum(w) if w is not None else float(n)
+    scaled_l2 = p.l2_leaf_reg * (sw / n) if n else p.l2_leaf_reg
+    lr = float(np.float32(p.learning_rate))  # boosting.rs:4958
+    K = int(n_classes)
+    cfg = DeviceTrainConfig(bootstrap_type=p.bootstrap_type, sample_rate=p.subsample, rng_seed=p.random_seed,
+                            bias=0.0, sample_from_host=False, bagging_temperature=p.bagging_temperature,
+                            device=device)
+    rt = B200MultiRuntime()
+    n_bins = max(len(b) for b in borders) + 1
+    ok = rt.begin_device_training_raw("MultiClass", p.depth, True, 1, p.score_function, cols, borders, w, n, F,
+                                      n_bins, lr, scaled_l2, cfg, approx_dim=K)
+    if not ok:
+        raise RuntimeError(f"device declined: {rt.decline_reason}")
+    T, D = p.iterations, p.depth
+    sf = np.zeros((T, D), dtype=np.int32)
+    sb = np.zeros((T, D), dtype=np.int32)
+    lv = np.zeros((T, 1 << D, K), dtype=np.float64)
+    st = np.zeros((T, n, K), dtype=np.float64) if staged else None
+    try:
+        for it in range(T):
+            tree = rt.grow_tree_on_device(None, y, [], family=("MultiOutput", None, K), leaf_of_bytes=0,
+                                          resident_approx=True)
+            for l, (f, b, _) in enumerate(tree.splits):
+                sf[it, l], sb[it, l] = f, b
+            lv[it] = tree.leaf_values.reshape(1 << D, K) * lr  # normalize_leaf_values
+            if staged:
+                st[it] = rt.resident_approx().T
+    finally:
+        rt.end_device_training()
+    return MultiClassModel([np.asarray(b, dtype=np.float64) for b in borders], sf, sb, lv, st)

@@ -17,7 +17,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "libcbgpu.so")
-SOURCES = ["kernels.cu", "session.cu", "noalloc.cu", "borders.cu", "apply.cu"]
+SOURCES = ["kernels.cu", "session.cu", "noalloc.cu", "borders.cu", "apply.cu", "multi.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -1,0 +1,862 @@
+// multi.cu -- the multi-output (MultiClass softmax) arm of the oblivious-tree
+// grow, behind the seam's FamilyTreeArgs::MultiOutput
+// (crates/cb-compute/src/runtime.rs:935-948): the approximant has K
+// dimensions, one tree serves all of them, and each leaf carries a K-vector.
+//
+// The reference's device session declines every multi-output fit
+// (crates/cb-backend/src/gpu_runtime/session.rs:1401-1467); its CPU branch
+// (crates/cb-train/src/boosting.rs:7400-8930 at approx_dimension K) is what
+// this arm reproduces, one CUDA stream per session:
+//
+//   per tree   mc_der_kernel       pending leaf update, softmax, weighted der1
+//              bootstrap           (the scalar path's kernels)
+//              mc_max / mc_pack    K + 1 score channels as int64 fixed point
+//   per level  mc_hist_kernel      (feature, channel, row chunk) blocks, the
+//                                  level's leaves x bins table in shared memory
+//              mc_prefix_kernel    exact int64 bin prefix sums
+//              mc_score_kernel     every (feature, border) candidate, multi-dim
+//                                  Cosine / L2 in dimension-then-leaf order
+//              mc_argmax_kernel    strict first-wins over (feature, border)
+//              mc_route_kernel     leaf |= (bin > border) << level
+//   per tree   mc_leafsum_kernel   int64 per-leaf sums of w*der1 and w*der2
+//              mc_newton_kernel    the trace-regularised symmetric Newton
+//                                  solve per leaf (Cholesky), x lr
+//
+// Histogram and leaf sums are exact integer sums of values rounded once to a
+// power-of-two fixed point, so results do not depend on the launch geometry or
+// atomic order; against the CPU's sequential f64 sums the difference is the
+// rounding of each value (2^-40 of the largest value or finer).  The host keeps
+// the main TFastRng64 stream replica with cb-train's draw accounting, as the
+// scalar session does.  One GPU per session; MVS and document sharding decline.
+#include <cfloat>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <vector>
+
+#include "../../include/cbgpu.h"
+#include "kernels.cuh"
+
+using namespace cbgpu;
+
+namespace cbgpu {
+int record_error(int code, const char* msg);  // session.cu: sets cbgpu_last_error()
+}
+
+namespace {
+
+constexpr int kMcMaxK = 16;
+constexpr int kMcMaxDepth = 10;
+constexpr int kMcChunk = 16384;                  // rows per histogram block
+constexpr size_t kMcSmemTable = 96 * 1024;       // shared table budget per block
+constexpr int kMcThreads = 256;
+
+enum : uint32_t { kMcErrNoCandidate = 1u << 0, kMcErrNonFinite = 1u << 1, kMcErrLeafRange = 1u << 2 };
+
+int mfail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    return cbgpu::record_error(code, buf);
+}
+
+#define MCU(call)                                                                             \
+    do {                                                                                      \
+        cudaError_t _e = (call);                                                              \
+        if (_e != cudaSuccess)                                                                \
+            return mfail(_e == cudaErrorMemoryAllocation ? CBGPU_ERR_OOM : CBGPU_ERR_CUDA,    \
+                         "%s failed: %s", #call, cudaGetErrorString(_e));                     \
+    } while (0)
+
+// Host replica of the main TFastRng64 stream with cb-train's call counter.
+struct McRng {
+    Rng64 r{};
+    uint64_t calls = 0;
+    uint64_t gen() {
+        ++calls;
+        return r.gen();
+    }
+    double real1() { return (double)(gen() >> 11) * (1.0 / 9007199254740991.0); }
+    void advance(uint64_t d) {
+        r.advance(d);
+        calls += d;
+    }
+    double std_normal() {  // normal.rs (Marsaglia polar)
+        for (;;) {
+            double x = real1() * 2.0 - 1.0;
+            double y = real1() * 2.0 - 1.0;
+            double rr = x * x + y * y;
+            if (!(rr > 1.0 || rr <= 0.0)) return x * std::sqrt(-2.0 * std::log(rr) / rr);
+        }
+    }
+};
+
+struct McSplit {
+    int32_t feature, bin;
+};
+
+// Per-tree device state read back once per tree.
+struct McState {
+    McSplit split[kMcMaxDepth];
+    uint32_t err;
+    uint32_t pad;
+    unsigned long long maxbits;  // bit pattern of max |score channel| (a non-negative double)
+    int32_t hist_shift;          // score channels are llrint(v * 2^hist_shift)
+    int32_t pad2;
+};
+
+// ---- kernels ---------------------------------------------------------------
+
+// Softmax probabilities of one object (loss.rs:424-455): max-subtracted exp,
+// sequential sum, division.
+__device__ __forceinline__ void mc_softmax(const double* __restrict__ approx, int64_t n, int64_t i, int K,
+                                           double* p) {
+    double mx = -INFINITY;
+    for (int d = 0; d < K; ++d) {
+        const double a = approx[(size_t)d * n + i];
+        p[d] = a;
+        if (a > mx) mx = a;
+    }
+    double s = 0.0;
+    for (int d = 0; d < K; ++d) {
+        p[d] = exp(__dsub_rn(p[d], mx));
+        s = __dadd_rn(s, p[d]);
+    }
+    for (int d = 0; d < K; ++d) p[d] = __ddiv_rn(p[d], s);
+}
+
+// approx += lr * leaf (the previous tree, when pending); wd1[d] = ([d == y] - p[d]) * w.
+__global__ void mc_der_kernel(int64_t n, int K, double* __restrict__ approx, const int32_t* __restrict__ target,
+                              const double* __restrict__ weight, const uint16_t* __restrict__ leaf,
+                              const double* __restrict__ lrv, int L, int pending, double* __restrict__ wd1,
+                              McState* __restrict__ ms) {
+    double p[kMcMaxK];
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        if (pending) {
+            const int q = leaf[i];
+            for (int d = 0; d < K; ++d)
+                approx[(size_t)d * n + i] = __dadd_rn(approx[(size_t)d * n + i], lrv[(size_t)d * L + q]);
+        }
+        mc_softmax(approx, n, i, K, p);
+        const double w = weight ? weight[i] : 1.0;
+        const int y = target[i];
+        bool finite = true;
+        for (int d = 0; d < K; ++d) {
+            double d1 = -p[d];
+            if (d == y) d1 = __dadd_rn(d1, 1.0);
+            const double v = __dmul_rn(d1, w);
+            finite &= isfinite(v);
+            wd1[(size_t)d * n + i] = v;
+        }
+        if (!finite) atomicOr(&ms->err, kMcErrNonFinite);
+    }
+}
+
+// score channels: c < K: wd1[c] * s, c == K: w * s (s = the bootstrap
+// multiplier; boosting.rs:7700-7732).  s_mode 0: 1, 1: f32 device sample,
+// 2: f64 host sample.
+__device__ __forceinline__ double mc_channel(int c, int K, int64_t n, int64_t i, const double* wd1,
+                                             const double* weight, int s_mode, const float* sw32,
+                                             const double* sw64) {
+    const double s = s_mode == 1 ? (double)sw32[i] : (s_mode == 2 ? sw64[i] : 1.0);
+    const double v = c < K ? wd1[(size_t)c * n + i] : (weight ? weight[i] : 1.0);
+    return __dmul_rn(v, s);
+}
+
+__global__ void mc_max_kernel(int64_t n, int K, const double* __restrict__ wd1, const double* __restrict__ weight,
+                              int s_mode, const float* __restrict__ sw32, const double* __restrict__ sw64,
+                              McState* __restrict__ ms) {
+    double mx = 0.0;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        for (int c = 0; c <= K; ++c) mx = fmax(mx, fabs(mc_channel(c, K, n, i, wd1, weight, s_mode, sw32, sw64)));
+    for (int o = 16; o > 0; o >>= 1) mx = fmax(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((threadIdx.x & 31) == 0 && mx > 0.0) atomicMax(&ms->maxbits, (unsigned long long)__double_as_longlong(mx));
+}
+
+// hist_shift: max |v| * 2^shift * n < 2^62, so no int64 sum over n rows overflows.
+__global__ void mc_shift_kernel(int64_t n, McState* ms) {
+    const double mx = __longlong_as_double((long long)ms->maxbits);
+    int e = 0;
+    if (mx > 0.0) frexp(mx, &e);  // mx < 2^e
+    int t = 0;
+    while (t < 62 && (1ll << t) < n) ++t;  // n <= 2^t
+    int sh = 61 - e - t;
+    if (sh > 1000) sh = 1000;
+    ms->hist_shift = sh;
+}
+
+__global__ void mc_pack_kernel(int64_t n, int K, const double* __restrict__ wd1, const double* __restrict__ weight,
+                               int s_mode, const float* __restrict__ sw32, const double* __restrict__ sw64,
+                               const McState* __restrict__ ms, long long* __restrict__ q) {
+    const int sh = ms->hist_shift;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        for (int c = 0; c <= K; ++c)
+            q[(size_t)c * n + i] = llrint(ldexp(mc_channel(c, K, n, i, wd1, weight, s_mode, sw32, sw64), sh));
+}
+
+// Level histogram: block (feature f, channel c, rows [r0, r0 + kMcChunk)) adds
+// q[c][row] into cell (leaf, f, bin, c) of hist[leaves][F][NB][C].  The
+// leaves x bins table sits in shared memory when it fits (smem > 0).
+__global__ void __launch_bounds__(kMcThreads)
+mc_hist_kernel(int64_t n, int F, int NB, int C, int leaves, const uint8_t* __restrict__ bins_fm,
+               const long long* __restrict__ q, const uint16_t* __restrict__ leaf,
+               unsigned long long* __restrict__ hist, int use_smem) {
+    extern __shared__ unsigned long long tab[];
+    const int f = blockIdx.x, c = blockIdx.y;
+    const int64_t r0 = (int64_t)blockIdx.z * kMcChunk;
+    const int64_t r1 = r0 + kMcChunk < n ? r0 + kMcChunk : n;
+    const int cells = leaves * NB;
+    if (use_smem) {
+        for (int k = threadIdx.x; k < cells; k += blockDim.x) tab[k] = 0ull;
+        __syncthreads();
+    }
+    const uint8_t* col = bins_fm + (size_t)f * (size_t)n;
+    const long long* qc = q + (size_t)c * (size_t)n;
+    for (int64_t i = r0 + threadIdx.x; i < r1; i += blockDim.x) {
+        const int lf = leaf[i];
+        const int b = col[i];
+        if (lf >= leaves || b >= NB) continue;
+        const long long v = qc[i];
+        if (v == 0) continue;
+        if (use_smem) atomicAdd(&tab[lf * NB + b], (unsigned long long)v);
+        else atomicAdd(&hist[(((size_t)lf * F + f) * NB + b) * C + c], (unsigned long long)v);
+    }
+    if (use_smem) {
+        __syncthreads();
+        for (int k = threadIdx.x; k < cells; k += blockDim.x) {
+            const unsigned long long v = tab[k];
+            if (v) {
+                const int lf = k / NB, b = k - lf * NB;
+                atomicAdd(&hist[(((size_t)lf * F + f) * NB + b) * C + c], v);
+            }
+        }
+    }
+}
+
+// Inclusive prefix over bins of every (leaf, feature, channel) row, in place.
+__global__ void mc_prefix_kernel(int leaves, int F, int NB, int C, unsigned long long* __restrict__ hist) {
+    const int64_t rows = (int64_t)leaves * F * C;
+    for (int64_t r = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; r < rows; r += (int64_t)gridDim.x * blockDim.x) {
+        const int c = (int)(r % C);
+        const int64_t lfq = r / C;  // leaf * F + f
+        unsigned long long* row = hist + (size_t)lfq * NB * C + c;
+        unsigned long long run = 0ull;
+        for (int b = 0; b < NB; ++b) {
+            run += row[(size_t)b * C];
+            row[(size_t)b * C] = run;
+        }
+    }
+}
+
+// calc_average (leaf.rs:161-175)
+__device__ __forceinline__ double mc_avg(double s, double w, double l2) {
+    return w > 0.0 ? __ddiv_rn(s, __dadd_rn(w, l2)) : 0.0;
+}
+
+// Score of candidate (f, b) over the 2P children of this level's P leaves:
+// multi_dim_split_score_into (score.rs:192-265), false children 0..P-1 then
+// true children, dimension-then-leaf order.
+__global__ void mc_score_kernel(int parents, int F, int NB, int K, const unsigned long long* __restrict__ pre,
+                                const int32_t* __restrict__ border_counts, const McState* __restrict__ ms,
+                                double l2, int score_fn, double* __restrict__ scores) {
+    const int64_t cand = (int64_t)F * NB;
+    const int C = K + 1;
+    const double inv = ldexp(1.0, -ms->hist_shift);
+    for (int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < cand; k += (int64_t)gridDim.x * blockDim.x) {
+        const int f = (int)(k / NB), b = (int)(k - (int64_t)f * NB);
+        if (b >= border_counts[f] || b >= NB - 1) {
+            scores[k] = -INFINITY;
+            continue;
+        }
+        double num = 0.0, den = 1e-100;
+        for (int pass = 0; pass < 2; ++pass) {
+            for (int d = 0; d < K; ++d) {
+                for (int side = 0; side < 2; ++side) {  // false children, then true children
+                    for (int q = 0; q < parents; ++q) {
+                        const unsigned long long* row = pre + ((size_t)q * F + f) * NB * C;
+                        const long long wp = (long long)row[(size_t)b * C + K];
+                        const long long wt = (long long)row[(size_t)(NB - 1) * C + K];
+                        const long long sp = (long long)row[(size_t)b * C + d];
+                        const long long st = (long long)row[(size_t)(NB - 1) * C + d];
+                        const double w = __dmul_rn((double)(side ? wt - wp : wp), inv);
+                        const double s = __dmul_rn((double)(side ? st - sp : sp), inv);
+                        const double avg = mc_avg(s, w, l2);
+                        if (pass == 0) num = __dadd_rn(num, __dmul_rn(avg, s));
+                        else den = __dadd_rn(den, __dmul_rn(__dmul_rn(avg, avg), w));
+                    }
+                }
+            }
+            if (score_fn == CBGPU_SCORE_L2) break;
+        }
+        scores[k] = score_fn == CBGPU_SCORE_L2 ? num : __ddiv_rn(num, sqrt(den));
+    }
+}
+
+// Strict first-wins argmax over (feature, border) (tree.rs:355-366): the
+// highest score, the lowest candidate index among equal scores.
+__global__ void __launch_bounds__(1024) mc_argmax_kernel(int64_t cand, int NB, const double* __restrict__ scores,
+                                                         int level, McState* __restrict__ ms) {
+    __shared__ double s_best[32];
+    __shared__ long long s_idx[32];
+    double best = -INFINITY;
+    long long idx = -1;
+    for (int64_t k = threadIdx.x; k < cand; k += blockDim.x) {
+        const double s = scores[k];
+        if (s > best) {  // k ascends per thread: the first maximum stays
+            best = s;
+            idx = k;
+        }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        const double ob = __shfl_xor_sync(0xffffffffu, best, o);
+        const long long oi = __shfl_xor_sync(0xffffffffu, idx, o);
+        if (oi >= 0 && (idx < 0 || ob > best || (ob == best && oi < idx))) {
+            best = ob;
+            idx = oi;
+        }
+    }
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) {
+        s_best[w] = best;
+        s_idx[w] = idx;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int k = 1; k < (int)(blockDim.x >> 5); ++k) {
+            const double ob = s_best[k];
+            const long long oi = s_idx[k];
+            if (oi >= 0 && (idx < 0 || ob > best || (ob == best && oi < idx))) {
+                best = ob;
+                idx = oi;
+            }
+        }
+        if (idx < 0) {
+            ms->err |= kMcErrNoCandidate;
+            ms->split[level] = McSplit{0, 0};
+        } else {
+            ms->split[level] = McSplit{(int32_t)(idx / NB), (int32_t)(idx % NB)};
+        }
+    }
+}
+
+// advance_leaf_only (tree.rs:1005-1016): the level's split is leaf bit `level`.
+__global__ void mc_route_kernel(int64_t n, int level, const uint8_t* __restrict__ bins_fm,
+                                const McState* __restrict__ ms, uint16_t* __restrict__ leaf) {
+    const McSplit sp = ms->split[level];
+    const uint8_t* col = bins_fm + (size_t)sp.feature * (size_t)n;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        if ((int)col[i] > sp.bin) leaf[i] = (uint16_t)(leaf[i] | (1u << level));
+}
+
+// Per-leaf sums of w*der1[d] (K) and w*der2 packed (pk) over ALL rows
+// (compute_softmax_leaf_deltas, boosting.rs:2610-2700), int64 fixed point at
+// 2^leaf_shift; table[L][K + pk] in shared memory when it fits.
+__global__ void __launch_bounds__(kMcThreads)
+mc_leafsum_kernel(int64_t n, int K, int L, const double* __restrict__ approx, const double* __restrict__ wd1,
+                  const double* __restrict__ weight, const uint16_t* __restrict__ leaf, int leaf_shift,
+                  unsigned long long* __restrict__ sums, int use_smem, McState* __restrict__ ms) {
+    extern __shared__ unsigned long long ltab[];
+    const int pk = K * (K + 1) / 2, W = K + pk;
+    if (use_smem) {
+        for (int k = threadIdx.x; k < L * W; k += blockDim.x) ltab[k] = 0ull;
+        __syncthreads();
+    }
+    unsigned long long* dst = use_smem ? ltab : sums;
+    double p[kMcMaxK];
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int q = leaf[i];
+        if (q >= L) {
+            atomicOr(&ms->err, kMcErrLeafRange);
+            continue;
+        }
+        unsigned long long* cell = dst + (size_t)q * W;
+        for (int d = 0; d < K; ++d)
+            atomicAdd(&cell[d], (unsigned long long)llrint(ldexp(wd1[(size_t)d * n + i], leaf_shift)));
+        mc_softmax(approx, n, i, K, p);
+        const double w = weight ? weight[i] : 1.0;
+        int j = 0;
+        for (int dy = 0; dy < K; ++dy) {
+            const double hyy = __dmul_rn(__dmul_rn(p[dy], __dsub_rn(p[dy], 1.0)), w);
+            atomicAdd(&cell[K + j++], (unsigned long long)llrint(ldexp(hyy, leaf_shift)));
+            for (int dx = dy + 1; dx < K; ++dx) {
+                const double hyx = __dmul_rn(__dmul_rn(p[dy], p[dx]), w);
+                atomicAdd(&cell[K + j++], (unsigned long long)llrint(ldexp(hyx, leaf_shift)));
+            }
+        }
+    }
+    if (use_smem) {
+        __syncthreads();
+        for (int k = threadIdx.x; k < L * W; k += blockDim.x)
+            if (ltab[k]) atomicAdd(&sums[k], ltab[k]);
+    }
+}
+
+// solve_symmetric_newton (leaf.rs:281-340) for leaf `threadIdx.x`: Rust
+// f32::max semantics for the trace regulariser, Cholesky (leaf.rs:360-420),
+// zeros on a non-positive pivot; delta x lr for the approximant.
+__global__ void mc_newton_kernel(int K, int L, const unsigned long long* __restrict__ sums, int leaf_shift,
+                                 double l2, double lr, double* __restrict__ leaf_raw, double* __restrict__ leaf_lrv) {
+    const int q = blockIdx.x * blockDim.x + threadIdx.x;
+    if (q >= L) return;
+    const int pk = K * (K + 1) / 2, W = K + pk;
+    const double inv = ldexp(1.0, -leaf_shift);
+    double H[kMcMaxK * kMcMaxK], Lm[kMcMaxK * kMcMaxK], y[kMcMaxK], x[kMcMaxK], g[kMcMaxK];
+    const unsigned long long* s = sums + (size_t)q * W;
+    for (int d = 0; d < K; ++d) g[d] = __dmul_rn((double)(long long)s[d], inv);
+    int j = 0;
+    for (int a = 0; a < K; ++a)
+        for (int b = a; b < K; ++b) {
+            const double v = __dmul_rn((double)(long long)s[K + j++], inv);
+            H[a * K + b] = v;
+            H[b * K + a] = v;
+        }
+    float mt = (float)l2;
+    for (int d = 0; d < K; ++d) {
+        const float t = (float)(-H[d * K + d]);
+        if (isnan(mt) || (!isnan(t) && t > mt)) mt = t;
+    }
+    float l2f = (float)l2, mtl = __fmul_rn(mt, FLT_EPSILON);
+    const float adjf = isnan(l2f) ? mtl : (isnan(mtl) ? l2f : (l2f > mtl ? l2f : mtl));
+    const double adj = (double)adjf;
+    for (int d = 0; d < K; ++d) H[d * K + d] = __dsub_rn(H[d * K + d], adj);
+    for (int k = 0; k < K * K; ++k) H[k] = -H[k];
+    for (int d = 0; d < K; ++d) g[d] = -g[d];
+    bool ok = true;
+    for (int k = 0; k < K * K; ++k) Lm[k] = 0.0;
+    for (int i = 0; i < K && ok; ++i)
+        for (int jj = 0; jj <= i && ok; ++jj) {
+            double sum = H[i * K + jj];
+            for (int p = 0; p < jj; ++p) sum = __dsub_rn(sum, __dmul_rn(Lm[i * K + p], Lm[jj * K + p]));
+            if (i == jj) {
+                if (sum <= 0.0) ok = false;
+                else Lm[i * K + jj] = sqrt(sum);
+            } else {
+                const double ljj = Lm[jj * K + jj];
+                if (ljj == 0.0) ok = false;
+                else Lm[i * K + jj] = __ddiv_rn(sum, ljj);
+            }
+        }
+    for (int i = 0; i < K && ok; ++i) {
+        double sum = g[i];
+        for (int p = 0; p < i; ++p) sum = __dsub_rn(sum, __dmul_rn(Lm[i * K + p], y[p]));
+        if (Lm[i * K + i] == 0.0) ok = false;
+        else y[i] = __ddiv_rn(sum, Lm[i * K + i]);
+    }
+    for (int i = K - 1; i >= 0 && ok; --i) {
+        double sum = y[i];
+        for (int p = i + 1; p < K; ++p) sum = __dsub_rn(sum, __dmul_rn(Lm[p * K + i], x[p]));
+        if (Lm[i * K + i] == 0.0) ok = false;
+        else x[i] = __ddiv_rn(sum, Lm[i * K + i]);
+    }
+    for (int d = 0; d < K; ++d) {
+        const double delta = ok ? -x[d] : 0.0;
+        leaf_raw[(size_t)q * K + d] = delta;                 // leaf-major, raw (the seam's layout)
+        leaf_lrv[(size_t)d * L + q] = __dmul_rn(delta, lr);  // dim-major, x lr (normalize_leaf_values)
+    }
+}
+
+__global__ void mc_leaf_export_kernel(int64_t n, const uint16_t* __restrict__ leaf, void* out, int bytes) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const uint32_t v = leaf[i];
+        if (bytes == 1) ((uint8_t*)out)[i] = (uint8_t)v;
+        else if (bytes == 2) ((uint16_t*)out)[i] = (uint16_t)v;
+        else ((uint32_t*)out)[i] = v;
+    }
+}
+
+__global__ void mc_apply_pending_kernel(int64_t n, int K, int L, double* __restrict__ approx,
+                                        const uint16_t* __restrict__ leaf, const double* __restrict__ lrv) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int q = leaf[i];
+        for (int d = 0; d < K; ++d)
+            approx[(size_t)d * n + i] = __dadd_rn(approx[(size_t)d * n + i], lrv[(size_t)d * L + q]);
+    }
+}
+
+unsigned grid_for(int64_t n, int threads = kMcThreads) {
+    int64_t b = (n + threads - 1) / threads;
+    if (b > 148 * 16) b = 148 * 16;
+    return (unsigned)(b < 1 ? 1 : b);
+}
+
+}  // namespace
+
+struct cbgpu_multi_session {
+    int device = 0, K = 0, depth = 0, F = 0, NB = 0, score_fn = 0, boot = 0, sample_from_host = 0;
+    float sample_rate = 1.0f, temp = 1.0f;
+    double lr = 0.0, l2 = 0.0;
+    int64_t n = 0;
+    int leaf_shift = 0;
+    bool target_ready = false, pending = false;
+    McRng rng;
+    cudaStream_t st = nullptr;
+    uint8_t* bins_fm = nullptr;
+    int32_t* d_bc = nullptr;
+    std::vector<int32_t> bc;
+    double *approx = nullptr, *weight = nullptr, *wd1 = nullptr, *sw64 = nullptr;
+    float* sw32 = nullptr;
+    int32_t* target = nullptr;
+    long long* q = nullptr;
+    uint16_t* leaf = nullptr;
+    unsigned long long *hist = nullptr, *sums = nullptr;
+    double *scores = nullptr, *leaf_raw = nullptr, *leaf_lrv = nullptr;
+    McState *d_ms = nullptr, *h_ms = nullptr;
+    TreeParams *d_tp = nullptr, *h_tp = nullptr;
+    double* h_raw = nullptr;
+    void* leaf_export = nullptr;
+    size_t hist_cells = 0;
+
+    ~cbgpu_multi_session() {
+        if (st) cudaStreamSynchronize(st);
+        cudaFree(bins_fm);
+        cudaFree(d_bc);
+        cudaFree(approx);
+        cudaFree(weight);
+        cudaFree(wd1);
+        cudaFree(sw64);
+        cudaFree(sw32);
+        cudaFree(target);
+        cudaFree(q);
+        cudaFree(leaf);
+        cudaFree(hist);
+        cudaFree(sums);
+        cudaFree(scores);
+        cudaFree(leaf_raw);
+        cudaFree(leaf_lrv);
+        cudaFree(d_ms);
+        cudaFree(d_tp);
+        cudaFree(leaf_export);
+        if (h_ms) cudaFreeHost(h_ms);
+        if (h_tp) cudaFreeHost(h_tp);
+        if (h_raw) cudaFreeHost(h_raw);
+        if (st) cudaStreamDestroy(st);
+    }
+};
+
+namespace {
+
+template <typename T>
+int mdalloc(T** p, size_t count) {
+    cudaError_t e = cudaMalloc((void**)p, sizeof(T) * (count ? count : 1));
+    if (e != cudaSuccess)
+        return mfail(e == cudaErrorMemoryAllocation ? CBGPU_ERR_OOM : CBGPU_ERR_CUDA, "cudaMalloc(%zu bytes): %s",
+                     sizeof(T) * count, cudaGetErrorString(e));
+    return CBGPU_OK;
+}
+
+#define MDA(p, count)                        \
+    do {                                     \
+        int _rc = mdalloc(&(p), (count));    \
+        if (_rc) return _rc;                 \
+    } while (0)
+
+template <typename T>
+int mhalloc(T** p, size_t count) {
+    cudaError_t e = cudaMallocHost((void**)p, sizeof(T) * (count ? count : 1));
+    if (e != cudaSuccess) return mfail(CBGPU_ERR_OOM, "cudaMallocHost: %s", cudaGetErrorString(e));
+    memset((void*)*p, 0, sizeof(T) * (count ? count : 1));
+    return CBGPU_OK;
+}
+
+int begin_impl(const cbgpu_begin_args* a, int32_t K, const float* const* cols, const double* borders_flat,
+               const int32_t* border_counts, cbgpu_multi_session* s) {
+    s->device = a->device;
+    s->K = K;
+    s->depth = a->depth;
+    s->F = a->n_features;
+    s->score_fn = a->score_function;
+    s->boot = a->bootstrap_type;
+    s->sample_from_host = a->sample_from_host;
+    s->sample_rate = a->sample_rate;
+    s->temp = a->bagging_temperature;
+    s->lr = a->learning_rate;
+    s->l2 = a->scaled_l2;
+    s->n = a->n;
+    s->rng.r = Rng64::from_seed(a->rng_seed);
+    s->bc.assign(border_counts, border_counts + s->F);
+    int maxb = 0;
+    for (int f = 0; f < s->F; ++f) maxb = std::max(maxb, (int)s->bc[(size_t)f]);
+    s->NB = maxb + 1;
+    const int64_t n = s->n;
+    const int F = s->F, C = K + 1, L = 1 << s->depth, pk = K * (K + 1) / 2;
+    MCU(cudaSetDevice(s->device));
+    MCU(cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking));
+    MDA(s->bins_fm, (size_t)F * n);
+    MDA(s->d_bc, F);
+    MDA(s->approx, (size_t)K * n);
+    MDA(s->wd1, (size_t)K * n);
+    MDA(s->q, (size_t)C * n);
+    MDA(s->target, n);
+    MDA(s->leaf, n);
+    MDA(s->sw32, n);
+    MDA(s->sw64, n);
+    s->hist_cells = (size_t)(L / 2) * F * s->NB * C;  // the deepest level has L/2 parents
+    MDA(s->hist, s->hist_cells);
+    MDA(s->scores, (size_t)F * s->NB);
+    MDA(s->sums, (size_t)L * (K + pk));
+    MDA(s->leaf_raw, (size_t)L * K);
+    MDA(s->leaf_lrv, (size_t)L * K);
+    MDA(s->d_ms, 1);
+    MDA(s->d_tp, 1);
+    {
+        int rc = mhalloc(&s->h_ms, 1);
+        if (rc) return rc;
+        rc = mhalloc(&s->h_tp, 1);
+        if (rc) return rc;
+        rc = mhalloc(&s->h_raw, (size_t)L * K);
+        if (rc) return rc;
+    }
+    MCU(cudaMemcpyAsync(s->d_bc, s->bc.data(), sizeof(int32_t) * F, cudaMemcpyHostToDevice, s->st));
+    MCU(cudaMemsetAsync(s->approx, 0, sizeof(double) * (size_t)K * n, s->st));  // bias 0 (boost_from_average off)
+    MCU(cudaMemsetAsync(s->leaf, 0, sizeof(uint16_t) * (size_t)n, s->st));
+    double max_w = 1.0;
+    if (a->weight) {
+        MDA(s->weight, n);
+        MCU(cudaMemcpyAsync(s->weight, a->weight, sizeof(double) * n, cudaMemcpyHostToDevice, s->st));
+        max_w = 0.0;
+        for (int64_t i = 0; i < n; ++i) max_w = std::max(max_w, std::fabs(a->weight[i]));
+    }
+    // leaf sums: |w * der1| <= max|w|, |w * der2| <= max|w| / 4: max * 2^shift * n < 2^62
+    {
+        int e = 0;
+        if (max_w > 0.0) std::frexp(max_w, &e);
+        int t = 0;
+        while (t < 62 && (1ll << t) < n) ++t;
+        s->leaf_shift = 61 - e - t;
+    }
+    // device quantization of each column (histogram.rs:159-165 bin_of)
+    float* d_col = nullptr;
+    double* d_b = nullptr;
+    uint32_t* d_err = nullptr;
+    MDA(d_col, n);
+    MDA(d_b, 256);
+    MDA(d_err, 1);
+    MCU(cudaMemsetAsync(d_err, 0, sizeof(uint32_t), s->st));
+    int64_t off = 0;
+    int rc = CBGPU_OK;
+    for (int f = 0; f < F && rc == CBGPU_OK; ++f) {
+        const int nb = s->bc[(size_t)f];
+        cudaError_t e = cudaMemcpyAsync(d_col, cols[f], sizeof(float) * n, cudaMemcpyHostToDevice, s->st);
+        if (e == cudaSuccess && nb > 0)
+            e = cudaMemcpyAsync(d_b, borders_flat + off, sizeof(double) * nb, cudaMemcpyHostToDevice, s->st);
+        if (e != cudaSuccess) rc = mfail(CBGPU_ERR_CUDA, "column upload: %s", cudaGetErrorString(e));
+        else launch_quantize_column(d_col, n, d_b, nb, s->bins_fm + (size_t)f * n, d_err, s->st);
+        off += nb;
+        // the staging buffers are reused by the next column: wait for this one
+        if (rc == CBGPU_OK && cudaStreamSynchronize(s->st) != cudaSuccess)
+            rc = mfail(CBGPU_ERR_CUDA, "quantize column %d failed", f);
+    }
+    cudaFree(d_col);
+    cudaFree(d_b);
+    cudaFree(d_err);
+    if (rc) return rc;
+    MCU(cudaStreamSynchronize(s->st));
+    return CBGPU_OK;
+}
+
+}  // namespace
+
+int cbgpu_multi_begin_raw(const cbgpu_begin_args* a, int32_t approx_dim, const float* const* float_columns,
+                          const double* borders_flat, const int32_t* border_counts, cbgpu_multi_session** out) {
+    if (!out) return mfail(CBGPU_ERR_INVALID, "multi_begin: out is NULL");
+    *out = nullptr;
+    if (!a || !border_counts || (a->n > 0 && !float_columns))
+        return mfail(CBGPU_ERR_INVALID, "multi_begin: bad arguments");
+    // the coverage this arm accepts; everything else declines to the CPU grower
+    if (a->loss != CBGPU_LOSS_MULTICLASS) return mfail(CBGPU_DECLINED, "multi_begin: loss is not MultiClass");
+    if (a->grow_policy != CBGPU_GROW_SYMMETRIC || !a->boosting_type_is_plain || a->fold_count != 1)
+        return mfail(CBGPU_DECLINED, "multi_begin: only Plain SymmetricTree with one fold");
+    if (a->score_function != CBGPU_SCORE_COSINE && a->score_function != CBGPU_SCORE_L2)
+        return mfail(CBGPU_DECLINED, "multi_begin: score function not covered");
+    if (a->random_strength != 0.0) return mfail(CBGPU_DECLINED, "multi_begin: random_strength != 0");
+    if (a->bootstrap_type == CBGPU_BOOT_MVS || a->bootstrap_type == CBGPU_BOOT_POISSON)
+        return mfail(CBGPU_DECLINED, "multi_begin: MVS / Poisson not covered on this arm");
+    if (a->world_size != 1) return mfail(CBGPU_DECLINED, "multi_begin: one GPU per multi-output session");
+    if (approx_dim < 2 || approx_dim > kMcMaxK)
+        return mfail(CBGPU_DECLINED, "multi_begin: approx_dim %d outside 2..%d", approx_dim, kMcMaxK);
+    if (a->depth < 1 || a->depth > kMcMaxDepth)
+        return mfail(CBGPU_DECLINED, "multi_begin: depth %d outside 1..%d", a->depth, kMcMaxDepth);
+    // histogram grids index row chunks in gridDim.z (at most 65535 chunks)
+    if (a->n < 1 || a->n > (int64_t)65535 * kMcChunk || a->n_features < 1)
+        return mfail(CBGPU_ERR_INVALID, "multi_begin: n must be 1..%lld and n_features >= 1",
+                     (long long)65535 * kMcChunk);
+    for (int f = 0; f < a->n_features; ++f)
+        if (border_counts[f] < 0 || border_counts[f] > 255)
+            return mfail(CBGPU_DECLINED, "multi_begin: feature %d has %d borders (> 255)", f, border_counts[f]);
+    {
+        int64_t off = 0;
+        for (int f = 0; f < a->n_features; ++f) {
+            for (int k = 1; k < border_counts[f]; ++k)
+                if (!(borders_flat[off + k - 1] < borders_flat[off + k]))
+                    return mfail(CBGPU_ERR_INVALID, "multi_begin: borders of feature %d are not ascending", f);
+            off += border_counts[f];
+        }
+    }
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) return mfail(CBGPU_ERR_NO_DEVICE, "no CUDA device");
+    if (a->device < 0 || a->device >= ndev) return mfail(CBGPU_ERR_INVALID, "multi_begin: bad device");
+    auto* s = new cbgpu_multi_session();
+    const int rc = begin_impl(a, approx_dim, float_columns, borders_flat, border_counts, s);
+    if (rc) {
+        delete s;
+        return rc;
+    }
+    *out = s;
+    return CBGPU_OK;
+}
+
+int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const double* target, int64_t n,
+                          const double* sample, int64_t sample_len, int32_t* split_feature, int32_t* split_bin,
+                          int32_t* n_splits, double* leaf_values, void* leaf_of, int32_t leaf_of_bytes) {
+    if (!s) return mfail(CBGPU_ERR_INVALID, "multi_grow: no session");
+    if (n != s->n) return mfail(CBGPU_ERR_INVALID, "LengthMismatch: n %lld != session n %lld", (long long)n,
+                                (long long)s->n);
+    if (sample_len != 0 && sample_len != n)
+        return mfail(CBGPU_ERR_INVALID, "LengthMismatch: sample length %lld", (long long)sample_len);
+    if (sample_len != 0 && !s->sample_from_host)
+        return mfail(CBGPU_ERR_INVALID, "Degenerate: a host sample without sample_from_host");
+    if (sample_len == 0 && s->sample_from_host)
+        return mfail(CBGPU_ERR_INVALID, "Degenerate: sample_from_host without a sample");
+    if (leaf_of && leaf_of_bytes != 0 && leaf_of_bytes != 1 && leaf_of_bytes != 2 && leaf_of_bytes != 4)
+        return mfail(CBGPU_ERR_INVALID, "multi_grow: leaf_of_bytes must be 1, 2 or 4");
+    const int K = s->K, D = s->depth, L = 1 << D, F = s->F, NB = s->NB, C = K + 1;
+    const int pk = K * (K + 1) / 2;
+    cudaStream_t st = s->st;
+    MCU(cudaSetDevice(s->device));
+    if (!s->target_ready) {
+        if (!target) return mfail(CBGPU_ERR_INVALID, "multi_grow: the first call needs the target");
+        std::vector<int32_t> cls((size_t)n);
+        for (int64_t i = 0; i < n; ++i) {
+            const double t = target[i];
+            if (!(t >= 0.0 && t < (double)K) || t != std::floor(t))
+                return mfail(CBGPU_ERR_INVALID, "multi_grow: target %g at row %lld is not a class index in 0..%d", t,
+                             (long long)i, K - 1);
+            cls[(size_t)i] = (int32_t)t;
+        }
+        MCU(cudaMemcpyAsync(s->target, cls.data(), sizeof(int32_t) * n, cudaMemcpyHostToDevice, st));
+        MCU(cudaStreamSynchronize(st));
+        s->target_ready = true;
+    }
+    if (approx_k) {
+        MCU(cudaMemcpyAsync(s->approx, approx_k, sizeof(double) * (size_t)K * n, cudaMemcpyHostToDevice, st));
+        s->pending = false;
+    }
+    // bootstrap: the host stream replica decides the draws (boosting.rs:6568-6660)
+    TreeParams& tp = *s->h_tp;
+    tp = TreeParams{};
+    int s_mode = 0, boot_mode = 0;
+    if (s->sample_from_host) {
+        MCU(cudaMemcpyAsync(s->sw64, sample, sizeof(double) * n, cudaMemcpyHostToDevice, st));
+        s_mode = 2;
+    } else if (s->boot != CBGPU_BOOT_NO) {
+        s->rng.gen();  // PRE_TREE_DRAWS = 2 (boosting.rs:59)
+        s->rng.gen();
+        if (s->boot == CBGPU_BOOT_BAYESIAN && s->temp != 0.0f) {
+            tp.boot_seed = s->rng.gen();
+            boot_mode = 1;
+            s_mode = 1;
+        } else if (s->boot == CBGPU_BOOT_BERNOULLI && (double)s->sample_rate < 1.0) {
+            tp.boot_base = s->rng.r;
+            s->rng.advance((uint64_t)n);
+            boot_mode = 2;
+            s_mode = 1;
+        }
+    }
+    MCU(cudaMemcpyAsync(s->d_tp, s->h_tp, sizeof(TreeParams), cudaMemcpyHostToDevice, st));
+    MCU(cudaMemsetAsync(s->d_ms, 0, sizeof(McState), st));
+    const unsigned g = grid_for(n);
+    mc_der_kernel<<<g, kMcThreads, 0, st>>>(n, K, s->approx, s->target, s->weight, s->leaf, s->leaf_lrv, L,
+                                            s->pending ? 1 : 0, s->wd1, s->d_ms);
+    MCU(cudaGetLastError());
+    s->pending = false;
+    // the previous tree's leaf ids are consumed: every row starts this tree in leaf 0
+    MCU(cudaMemsetAsync(s->leaf, 0, sizeof(uint16_t) * (size_t)n, st));
+    if (boot_mode) launch_bootstrap(boot_mode, n, 0, s->d_tp, (double)s->sample_rate, s->temp, s->sw32, st);
+    mc_max_kernel<<<g, kMcThreads, 0, st>>>(n, K, s->wd1, s->weight, s_mode, s->sw32, s->sw64, s->d_ms);
+    mc_shift_kernel<<<1, 1, 0, st>>>(n, s->d_ms);
+    mc_pack_kernel<<<g, kMcThreads, 0, st>>>(n, K, s->wd1, s->weight, s_mode, s->sw32, s->sw64, s->d_ms, s->q);
+    MCU(cudaGetLastError());
+    const unsigned chunks = (unsigned)((n + kMcChunk - 1) / kMcChunk);
+    for (int l = 0; l < D; ++l) {
+        const int leaves = 1 << l;
+        const size_t cells = (size_t)leaves * F * NB * C;
+        MCU(cudaMemsetAsync(s->hist, 0, sizeof(unsigned long long) * cells, st));
+        const size_t tab = (size_t)leaves * NB * sizeof(unsigned long long);
+        const int use_smem = tab <= kMcSmemTable ? 1 : 0;
+        if (use_smem && tab > 48 * 1024)
+            MCU(cudaFuncSetAttribute(mc_hist_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tab));
+        mc_hist_kernel<<<dim3((unsigned)F, (unsigned)C, chunks), kMcThreads, use_smem ? tab : 0, st>>>(
+            n, F, NB, C, leaves, s->bins_fm, s->q, s->leaf, s->hist, use_smem);
+        MCU(cudaGetLastError());
+        mc_prefix_kernel<<<grid_for((int64_t)leaves * F * C), kMcThreads, 0, st>>>(leaves, F, NB, C, s->hist);
+        mc_score_kernel<<<grid_for((int64_t)F * NB), kMcThreads, 0, st>>>(leaves, F, NB, K, s->hist, s->d_bc, s->d_ms,
+                                                                          s->l2, s->score_fn, s->scores);
+        mc_argmax_kernel<<<1, 1024, 0, st>>>((int64_t)F * NB, NB, s->scores, l, s->d_ms);
+        mc_route_kernel<<<g, kMcThreads, 0, st>>>(n, l, s->bins_fm, s->d_ms, s->leaf);
+        MCU(cudaGetLastError());
+    }
+    // leaf values from the unsampled channels (boosting.rs:2610-2700)
+    const size_t ltab = (size_t)L * (K + pk) * sizeof(unsigned long long);
+    const int luse = ltab <= kMcSmemTable ? 1 : 0;
+    MCU(cudaMemsetAsync(s->sums, 0, ltab, st));
+    if (luse && ltab > 48 * 1024)
+        MCU(cudaFuncSetAttribute(mc_leafsum_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ltab));
+    mc_leafsum_kernel<<<g, kMcThreads, luse ? ltab : 0, st>>>(n, K, L, s->approx, s->wd1, s->weight, s->leaf,
+                                                             s->leaf_shift, s->sums, luse, s->d_ms);
+    mc_newton_kernel<<<(L + 63) / 64, 64, 0, st>>>(K, L, s->sums, s->leaf_shift, s->l2, s->lr, s->leaf_raw,
+                                                   s->leaf_lrv);
+    MCU(cudaGetLastError());
+    MCU(cudaMemcpyAsync(s->h_raw, s->leaf_raw, sizeof(double) * (size_t)L * K, cudaMemcpyDeviceToHost, st));
+    MCU(cudaMemcpyAsync(s->h_ms, s->d_ms, sizeof(McState), cudaMemcpyDeviceToHost, st));
+    if (leaf_of && leaf_of_bytes) {
+        if (!s->leaf_export) MDA(*(uint32_t**)&s->leaf_export, n);
+        mc_leaf_export_kernel<<<g, kMcThreads, 0, st>>>(n, s->leaf, s->leaf_export, leaf_of_bytes);
+        MCU(cudaMemcpyAsync(leaf_of, s->leaf_export, (size_t)leaf_of_bytes * n, cudaMemcpyDeviceToHost, st));
+    }
+    // the RNG phase after the tree (boosting.rs:7267-7300, device_draw_replay.rs)
+    if (!s->sample_from_host && s->boot != CBGPU_BOOT_NO) {
+        for (int l = 0; l < D; ++l) {
+            for (int f = 0; f < F; ++f) (void)s->rng.real1();
+            (void)s->rng.gen();
+            for (int f = 0; f < F; ++f) (void)s->rng.std_normal();
+        }
+        s->rng.gen();  // POST_TREE_EXTRA_DRAWS = 2
+        s->rng.gen();
+    }
+    MCU(cudaStreamSynchronize(st));
+    const McState& m = *s->h_ms;
+    if (m.err & kMcErrNoCandidate) return mfail(CBGPU_ERR_DEVICE, "Degenerate: no split candidate available");
+    if (m.err) return mfail(CBGPU_ERR_DEVICE, "multi_grow: device error word 0x%x", m.err);
+    for (int l = 0; l < D; ++l) {
+        if (split_feature) split_feature[l] = m.split[l].feature;
+        if (split_bin) split_bin[l] = m.split[l].bin;
+    }
+    if (n_splits) *n_splits = D;
+    if (leaf_values) memcpy(leaf_values, s->h_raw, sizeof(double) * (size_t)L * K);
+    s->pending = true;
+    return CBGPU_OK;
+}
+
+int cbgpu_multi_approx(cbgpu_multi_session* s, double* out_dim_major, int64_t n) {
+    if (!s || !out_dim_major || n != s->n) return mfail(CBGPU_ERR_INVALID, "multi_approx: bad arguments");
+    MCU(cudaSetDevice(s->device));
+    if (s->pending) {
+        mc_apply_pending_kernel<<<grid_for(n), kMcThreads, 0, s->st>>>(n, s->K, 1 << s->depth, s->approx, s->leaf,
+                                                                         s->leaf_lrv);
+        MCU(cudaGetLastError());
+        s->pending = false;
+    }
+    MCU(cudaMemcpyAsync(out_dim_major, s->approx, sizeof(double) * (size_t)s->K * n, cudaMemcpyDeviceToHost, s->st));
+    MCU(cudaStreamSynchronize(s->st));
+    return CBGPU_OK;
+}
+
+int cbgpu_multi_end(cbgpu_multi_session* s) {
+    if (!s) return CBGPU_OK;
+    cudaSetDevice(s->device);
+    delete s;
+    return CBGPU_OK;
+}

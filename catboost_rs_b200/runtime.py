@@ -18,7 +18,7 @@ import numpy as np
 
 from . import _lib
 
-LOSS = {"RMSE": 0, "Rmse": 0, "Logloss": 1, "CrossEntropy": 2}
+LOSS = {"RMSE": 0, "Rmse": 0, "Logloss": 1, "CrossEntropy": 2, "MultiClass": 3}
 SCORE = {"Cosine": 0, "L2": 1, "SolarL2": 2, "NewtonL2": 3, "NewtonCosine": 4, "LOOL2": 5, "SatL2": 6}
 BOOT = {"No": 0, "Bayesian": 1, "Bernoulli": 2, "MVS": 3, "Mvs": 3, "Poisson": 4}
 GROW = {"SymmetricTree": 0, "Depthwise": 1, "Lossguide": 2, "Region": 3}
@@ -279,6 +279,92 @@ class B200Runtime:
         out = np.zeros(5, dtype=np.uint64)
         _lib.check(self._L.cbgpu_session_rng_state(self._s, _ptr(out)))
         return tuple(int(x) for x in out[:4]), int(out[4])
+
+
+class B200MultiRuntime(B200Runtime):
+    """The seam's multi-output family (FamilyTreeArgs::MultiOutput,
+    runtime.rs:935-948) for MultiClass: the same method names as the scalar
+    runtime, with a K-dimensional approximant (dim-major, approx_k[d * n + i])
+    and leaf_count x K leaf blocks.  Backed by cbgpu_multi_* (one GPU)."""
+
+    def __init__(self):
+        super().__init__()
+        self.approx_dim = 0
+
+    def begin_device_training_raw(self, loss, depth, boosting_type_is_plain, fold_count, score_function,
+                                  float_columns, feature_borders, weight, n, n_features, n_bins,
+                                  learning_rate, scaled_l2, config: DeviceTrainConfig, approx_dim: int = 2) -> bool:
+        self.end_device_training()
+        cols = [np.ascontiguousarray(c, dtype=np.float32) for c in float_columns]
+        if len(cols) != n_features or any(c.size != n for c in cols):
+            raise _lib.CbGpuError(_lib.ERR_INVALID, "LengthMismatch: float_columns")
+        counts = np.array([len(b) for b in feature_borders], dtype=np.int32)
+        flat = np.ascontiguousarray(
+            np.concatenate([np.asarray(b, dtype=np.float64) for b in feature_borders])
+            if counts.sum() else np.zeros(1), dtype=np.float64)
+        colptrs = (C.c_void_p * max(1, len(cols)))(*[c.ctypes.data for c in cols])
+        a = self._args(loss, depth, boosting_type_is_plain, fold_count, score_function, weight, n,
+                       n_features, n_bins, learning_rate, scaled_l2, config)
+        rc = self._L.cbgpu_multi_begin_raw(C.byref(a), int(approx_dim), colptrs, _ptr(flat), _ptr(counts),
+                                           C.byref(self._s))
+        ok = self._finish_begin(rc, n, depth)
+        self.approx_dim = int(approx_dim) if ok else 0
+        return ok
+
+    def begin_device_training(self, *args, **kwargs) -> bool:
+        raise _lib.CbGpuError(_lib.DECLINED, "the multi-output arm quantizes on the device (begin_raw)")
+
+    def grow_tree_on_device(self, approx, target, sample, family=None, leaf_of_bytes: int = 4,
+                            resident_approx: bool = False) -> Optional[DeviceGrownTree]:
+        """family = ("MultiOutput", approx_k, approx_dim); approx_k None with
+        resident_approx uses the session's own approximant."""
+        if not self._s:
+            return None
+        K, n, D = self.approx_dim, self.n, self.depth
+        ak = None
+        if family is not None:
+            kind, fam_approx, fam_dim = family
+            if kind != "MultiOutput" or int(fam_dim) != K:
+                raise _lib.CbGpuError(_lib.DECLINED, f"family {kind} / dim {fam_dim} not covered")
+            if not resident_approx and fam_approx is not None:
+                ak = np.ascontiguousarray(fam_approx, dtype=np.float64).reshape(-1)
+                if ak.size != K * n:
+                    raise _lib.CbGpuError(_lib.ERR_INVALID, f"LengthMismatch: approx_k has {ak.size}, expected {K * n}")
+        t = None if target is None else np.ascontiguousarray(target, dtype=np.float64)
+        s = None if sample is None or len(sample) == 0 else np.ascontiguousarray(sample, dtype=np.float64)
+        if t is not None and t.size != n:
+            raise _lib.CbGpuError(_lib.ERR_INVALID, f"LengthMismatch: target has {t.size}, expected {n}")
+        sf = np.empty(D, dtype=np.int32)
+        sb = np.empty(D, dtype=np.int32)
+        ns = np.zeros(1, dtype=np.int32)
+        lv = np.empty((1 << D) * K, dtype=np.float64)
+        lo = None
+        if leaf_of_bytes:
+            lo = np.empty(n, dtype={1: np.uint8, 2: np.uint16, 4: np.uint32}[leaf_of_bytes])
+        rc = self._L.cbgpu_multi_grow_tree(self._s, _ptr(ak), _ptr(t), n, _ptr(s), 0 if s is None else s.size,
+                                           _ptr(sf), _ptr(sb), _ptr(ns), _ptr(lv), _ptr(lo),
+                                           leaf_of_bytes if lo is not None else 0)
+        _lib.check(rc)
+        k = int(ns[0])
+        return DeviceGrownTree(splits=[(int(sf[i]), int(sb[i]), False) for i in range(k)], leaf_values=lv,
+                               approx_dim=K, leaf_of=lo if lo is not None else np.zeros(0, dtype=np.uint32))
+
+    def end_device_training(self) -> None:
+        if self._s:
+            self._L.cbgpu_multi_end(self._s)
+            self._s = C.c_void_p(None)
+
+    def resident_approx(self) -> np.ndarray:
+        """The resident approximant, dim-major [K, n]."""
+        out = np.empty((self.approx_dim, self.n), dtype=np.float64)
+        _lib.check(self._L.cbgpu_multi_approx(self._s, _ptr(out), self.n))
+        return out
+
+    def device_bins(self, n_features):
+        raise NotImplementedError("multi-output sessions do not export their bins")
+
+    def last_sample(self):
+        raise NotImplementedError("multi-output sessions do not export their sample")
 
 
 # ---- building blocks -------------------------------------------------------

@@ -44,8 +44,12 @@ typedef enum {
     CBGPU_ERR_NO_DEVICE = 7   /* no CUDA device / library built without one */
 } cbgpu_status;
 
-/* Loss (runtime.rs:57-70): only the device-covered subset. */
-typedef enum { CBGPU_LOSS_RMSE = 0, CBGPU_LOSS_LOGLOSS = 1, CBGPU_LOSS_CROSSENTROPY = 2 } cbgpu_loss;
+/* Loss (runtime.rs:57-70): only the device-covered subset.  MultiClass is
+ * served by the multi-output session (cbgpu_multi_begin_raw); the scalar
+ * session declines it. */
+typedef enum {
+    CBGPU_LOSS_RMSE = 0, CBGPU_LOSS_LOGLOSS = 1, CBGPU_LOSS_CROSSENTROPY = 2, CBGPU_LOSS_MULTICLASS = 3
+} cbgpu_loss;
 
 /* EScoreFunction (runtime.rs:834-864); Cosine is the default. */
 typedef enum {
@@ -239,6 +243,47 @@ CBGPU_API int cbgpu_bootstrap_weights(int32_t type, int64_t n, int64_t row_offse
 CBGPU_API int cbgpu_histogram_noalloc(const uint8_t* d_bins_row_major, int64_t n, int32_t n_features,
                                       int32_t row_stride, int32_t n_bins, const double* d_g,
                                       const double* d_h, double* d_out_hist, void* stream);
+
+/* ---- multi-output (MultiClass) arm ------------------------------------- */
+
+/* The seam's FamilyTreeArgs::MultiOutput family (runtime.rs:935-948) for
+ * MultiClass (softmax, Newton leaves): one oblivious tree per iteration, a
+ * K-vector per leaf.  The reference's device session declines every
+ * multi-output fit (crates/cb-backend/src/gpu_runtime/session.rs:1401-1467)
+ * and cb-train grows these trees on the CPU
+ * (crates/cb-train/src/boosting.rs:7400-8930 at approx_dimension K); this arm
+ * reproduces that CPU branch on one GPU.
+ *
+ * cbgpu_multi_begin_raw: begin_device_training_raw's arguments (loss must be
+ * CBGPU_LOSS_MULTICLASS; world_size 1) plus approx_dim = K (2..16).  Declines
+ * (CBGPU_DECLINED) outside SymmetricTree / Plain / one fold / Cosine-L2 /
+ * bootstrap No-Bayesian-Bernoulli / depth <= 10 / <= 255 borders.  The
+ * approximant starts at 0 (MultiClass has no boost_from_average). */
+typedef struct cbgpu_multi_session cbgpu_multi_session;
+CBGPU_API int cbgpu_multi_begin_raw(const cbgpu_begin_args* args, int32_t approx_dim,
+                                    const float* const* float_columns, const double* borders_flat,
+                                    const int32_t* border_counts, cbgpu_multi_session** out);
+
+/* grow_tree_on_device with FamilyTreeArgs::MultiOutput (runtime.rs:1629):
+ *  approx_k  [K * n] DIM-major approximant (approx_k[d * n + i]) or NULL for
+ *            the resident approximant (advanced by learning_rate * leaf);
+ *  target    [n] class index per object as a double (0..K-1), read on the
+ *            first call;
+ *  sample    the host bootstrap multiplier, as for cbgpu_grow_tree;
+ *  leaf_values [2^depth * K] LEAF-major raw deltas (DeviceGrownTree's
+ *            leaf_count x approx_dim block, runtime.rs:1008-1024), not scaled
+ *            by learning_rate; the rest as cbgpu_grow_tree. */
+CBGPU_API int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const double* target,
+                                    int64_t n, const double* sample, int64_t sample_len, int32_t* split_feature,
+                                    int32_t* split_bin, int32_t* n_splits, double* leaf_values, void* leaf_of,
+                                    int32_t leaf_of_bytes);
+
+/* The resident approximant, DIM-major [K * n] (flushes the pending update).
+ * No counterpart in the reference. */
+CBGPU_API int cbgpu_multi_approx(cbgpu_multi_session* s, double* out_dim_major, int64_t n);
+
+/* end_device_training for a multi-output session. */
+CBGPU_API int cbgpu_multi_end(cbgpu_multi_session* s);
 
 /* ---- fit preparation -------------------------------------------------- */
 
