@@ -136,3 +136,27 @@ def test_quantize_nan_modes():
     b_max = [np.array([0.0, 1.0, fmax])]
     assert oracle.quantize(cols, b_min).tolist() == [[0, 1, 1, 2, 3]]
     assert oracle.quantize(cols, b_max).tolist() == [[3, 0, 0, 1, 2]]
+
+
+# The numeric_tiny fixtures again, now with the FULL standalone GreedyLogSum
+# border set (border_count 254, nan_mode Min; 49 borders per feature, pinned by
+# tests/test_oracle_borders.py) instead of the model's training-pruned
+# borders, so every candidate upstream scored competes in the oracle's search.
+FULL_BORDER_SCENARIOS = ["regression_skeleton", "binclf_skeleton", "regularization_l2",
+                         "regularization_bagging_temp", "regularization_random_strength_bernoulli"]
+
+
+@pytest.mark.parametrize("name", FULL_BORDER_SCENARIOS)
+def test_oracle_matches_upstream_with_full_border_set(name):
+    sc = load_scenario(name)
+    X = sc["X"]
+    full = [oracle.select_borders(X[:, f], 254, "GreedyLogSum", "Min") for f in range(X.shape[1])]
+    assert [len(b) for b in full] == [49] * X.shape[1]
+    sc["borders"] = full
+    sc["border_counts"] = np.array([len(b) for b in full], dtype=np.int32)
+    fit = _oracle_fit(sc)
+    np.testing.assert_array_equal(fit.split_feature, sc["split_feature"])
+    got_border = np.array([[full[f][b] for f, b in zip(rf, rb)] for rf, rb in zip(fit.split_feature, fit.split_bin)])
+    np.testing.assert_array_equal(got_border.astype(np.float32), sc["split_border"].astype(np.float32))
+    assert np.max(np.abs(fit.leaf_values - sc["leaf_values"])) <= TOL
+    assert np.max(np.abs(fit.staged - sc["staged"])) <= TOL
