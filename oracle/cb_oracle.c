@@ -616,6 +616,18 @@ static int search_tree(const search_ctx* c, int32_t* feat, int32_t* sbin, int32_
     return taken;
 }
 
+/* The search above for callers outside this file (the grouped-loss loop in
+ * cb_oracle_rank.c): score channels g/h, the RNG-drawing path when `draws`. */
+int orc_search_tree(int64_t n, int32_t F, int32_t n_bins, int32_t depth, int32_t score_fn, const uint8_t* bins,
+                    const int32_t* border_counts, const double* g, const double* h, double l2, int32_t draws,
+                    orc_rng* rng, int32_t* feat, int32_t* sbin, int32_t* leaf_of, int32_t* err) {
+    search_ctx sc = {n, F, n_bins, depth, score_fn, bins, border_counts, g, h, l2, draws, rng, 0.0};
+    int e = 0;
+    int taken = search_tree(&sc, feat, sbin, leaf_of, &e);
+    *err = e;
+    return taken;
+}
+
 /* ======================================================================== */
 /* boosting loop -- crates/cb-train/src/boosting.rs CPU branch               */
 /* (:1871 starting approx, :7400-8930 per-iteration body, :55-69 draws)      */

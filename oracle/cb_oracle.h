@@ -181,6 +181,46 @@ int orc_train_multiclass(const orc_multi_args* a, orc_multi_out* o);
 void orc_solve_symmetric_newton(const double* sum_der, const double* sum_der2_packed, int32_t k,
                                 double scaled_l2, double* out);
 
+/* ---- grouped (ranking) losses, pointwise histograms -------------------- */
+enum { ORC_RANK_QUERYRMSE = 0, ORC_RANK_PAIRLOGIT = 1 };
+
+/* The greedy oblivious search of the scalar loop, exported for the grouped
+ * loop: returns the splits taken; leaf_of gets the final leaf ids. */
+int orc_search_tree(int64_t n, int32_t F, int32_t n_bins, int32_t depth, int32_t score_fn, const uint8_t* bins,
+                    const int32_t* border_counts, const double* g, const double* h, double l2, int32_t draws,
+                    orc_rng* rng, int32_t* feat, int32_t* sbin, int32_t* leaf_of, int32_t* err);
+
+typedef struct {
+    int64_t n;
+    int32_t n_features;
+    const uint8_t* bins_fm;        /* [F][n] */
+    const int32_t* border_counts;  /* [F] */
+    const double* target;          /* [n] */
+    const double* weights;         /* [n] or NULL */
+    int32_t loss;                  /* ORC_RANK_* */
+    int32_t n_groups;
+    const int64_t* group_offsets;  /* [n_groups + 1] contiguous groups over object order */
+    int64_t n_pairs;
+    const int64_t* pair_winner;    /* [n_pairs] global object ids (PairLogit) */
+    const int64_t* pair_loser;
+    int32_t depth;
+    int32_t iterations;
+    double learning_rate;
+    double l2_leaf_reg;
+    int32_t score_function;
+    uint64_t random_seed;
+} orc_rank_args;
+
+typedef struct {
+    int32_t* split_feature;  /* [iterations * depth] */
+    int32_t* split_bin;
+    double* leaf_values;     /* [iterations * 2^depth] centred (PairLogit) and learning-rate scaled */
+    double* raw_leaf_values; /* [iterations * 2^depth] the Newton deltas before normalisation, or NULL */
+    double* staged;          /* [iterations * n] or NULL */
+} orc_rank_out;
+
+int orc_train_ranking(const orc_rank_args* a, orc_rank_out* o);
+
 #ifdef __cplusplus
 }
 #endif

@@ -73,6 +73,25 @@ class _MultiOut(C.Structure):
                 ("leaf_values", C.c_void_p), ("staged", C.c_void_p), ("final_approx", C.c_void_p)]
 
 
+class _RankArgs(C.Structure):
+    _fields_ = [
+        ("n", C.c_int64), ("n_features", C.c_int32), ("bins_fm", C.c_void_p), ("border_counts", C.c_void_p),
+        ("target", C.c_void_p), ("weights", C.c_void_p), ("loss", C.c_int32), ("n_groups", C.c_int32),
+        ("group_offsets", C.c_void_p), ("n_pairs", C.c_int64), ("pair_winner", C.c_void_p),
+        ("pair_loser", C.c_void_p), ("depth", C.c_int32), ("iterations", C.c_int32),
+        ("learning_rate", C.c_double), ("l2_leaf_reg", C.c_double), ("score_function", C.c_int32),
+        ("random_seed", C.c_uint64),
+    ]
+
+
+class _RankOut(C.Structure):
+    _fields_ = [("split_feature", C.c_void_p), ("split_bin", C.c_void_p), ("leaf_values", C.c_void_p),
+                ("raw_leaf_values", C.c_void_p), ("staged", C.c_void_p)]
+
+
+RANK_LOSS = {"QueryRMSE": 0, "PairLogit": 1}
+
+
 def lib():
     global _lib
     if _lib is None:
@@ -114,6 +133,8 @@ def lib():
         L.orc_train_multiclass.argtypes = [P(_MultiArgs), P(_MultiOut)]
         L.orc_train_multiclass.restype = C.c_int
         L.orc_solve_symmetric_newton.argtypes = [C.c_void_p, C.c_void_p, C.c_int32, C.c_double, C.c_void_p]
+        L.orc_train_ranking.argtypes = [P(_RankArgs), P(_RankOut)]
+        L.orc_train_ranking.restype = C.c_int
         L.orc_train.argtypes = [P(_TrainArgs), P(_TrainOut)]
         L.orc_train.restype = C.c_int
         _lib = L
@@ -366,3 +387,40 @@ def solve_symmetric_newton(sum_der, sum_der2_packed, scaled_l2):
     out = np.empty(d.size, dtype=np.float64)
     lib().orc_solve_symmetric_newton(_p(d), _p(h), d.size, scaled_l2, _p(out))
     return out
+
+
+@dataclass
+class OracleRankFit:
+    split_feature: np.ndarray   # [iters, depth]
+    split_bin: np.ndarray       # [iters, depth]
+    leaf_values: np.ndarray     # [iters, 2^depth] normalised and learning-rate scaled
+    raw_leaf_values: np.ndarray  # [iters, 2^depth] Newton deltas
+    staged: np.ndarray | None   # [iters, n]
+
+
+def train_ranking(bins_fm, border_counts, target, group_offsets, *, loss="QueryRMSE", pairs=None, depth=6,
+                  iterations=10, learning_rate=0.1, l2_leaf_reg=3.0, score_function="Cosine", random_seed=0,
+                  weights=None, staged=True) -> OracleRankFit:
+    """The reference's grouped-loss CPU loop (QueryRMSE / PairLogit, pointwise histograms, Newton leaves)."""
+    bins = np.ascontiguousarray(bins_fm, dtype=np.uint8)
+    F, n = bins.shape
+    bc = np.ascontiguousarray(border_counts, dtype=np.int32)
+    t = np.ascontiguousarray(target, dtype=np.float64)
+    go = np.ascontiguousarray(group_offsets, dtype=np.int64)
+    pr = np.zeros((0, 2), dtype=np.int64) if pairs is None else np.ascontiguousarray(pairs, dtype=np.int64)
+    pw = np.ascontiguousarray(pr[:, 0])
+    pl = np.ascontiguousarray(pr[:, 1])
+    w = None if weights is None else np.ascontiguousarray(weights, dtype=np.float64)
+    L = 1 << depth
+    sf = np.empty((iterations, depth), dtype=np.int32)
+    sb = np.empty((iterations, depth), dtype=np.int32)
+    lv = np.empty((iterations, L), dtype=np.float64)
+    raw = np.empty((iterations, L), dtype=np.float64)
+    st = np.empty((iterations, n), dtype=np.float64) if staged else None
+    args = _RankArgs(n, F, _p(bins), _p(bc), _p(t), _p(w), RANK_LOSS[loss], go.size - 1, _p(go), pw.size, _p(pw),
+                     _p(pl), depth, iterations, learning_rate, l2_leaf_reg, SCORE[score_function], random_seed)
+    out = _RankOut(_p(sf), _p(sb), _p(lv), _p(raw), _p(st))
+    rc = lib().orc_train_ranking(C.byref(args), C.byref(out))
+    if rc != 0:
+        raise RuntimeError(f"orc_train_ranking failed rc={rc}")
+    return OracleRankFit(sf, sb, lv, raw, st)

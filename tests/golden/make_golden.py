@@ -233,6 +233,35 @@ def multiclass_fixture(ref):
     return "multiclass_softmax"
 
 
+def ranking_fixtures(ref):
+    """Upstream QueryRMSE / PairLogit fixtures on the reference's frozen ranking
+    corpus (12 objects, 5 contiguous groups, 7 explicit pairs): inputs, group
+    offsets, pairs, and per loss the trees, leaf values and staged approximants."""
+    fx = os.path.join(ref, "crates/cb-oracle/fixtures/ranking_corpus")
+    gid = np.load(os.path.join(fx, "inputs/group_id.npy"))
+    offsets = np.concatenate([[0], np.flatnonzero(np.diff(gid)) + 1, [gid.size]]).astype(np.int64)
+    arrays = dict(X=np.load(os.path.join(fx, "inputs/X.npy")).astype(np.float32),
+                  y=np.load(os.path.join(fx, "inputs/y.npy")).astype(np.float64), group_offsets=offsets,
+                  pairs=np.load(os.path.join(fx, "inputs/pairs.npy")).astype(np.int64))
+    losses = []
+    for loss in ("QueryRMSE", "PairLogit"):
+        cfg = json.loads(_read(os.path.join(fx, loss, "config.json")))
+        model = json.loads(_read(os.path.join(fx, loss, "model.json")))
+        trees = model["oblivious_trees"]
+        arrays[f"{loss}__split_feature"] = np.array([[s["float_feature_index"] for s in t["splits"]] for t in trees],
+                                                    dtype=np.int32)
+        arrays[f"{loss}__split_border"] = np.array([[s["border"] for s in t["splits"]] for t in trees])
+        arrays[f"{loss}__leaf_values"] = np.array([t["leaf_values"] for t in trees], dtype=np.float64)
+        arrays[f"{loss}__staged"] = np.load(os.path.join(fx, loss, "staged.npy")).reshape(len(trees), -1)
+        arrays[f"{loss}__params"] = np.array(json.dumps({
+            "depth": int(cfg["depth"]), "iterations": int(cfg["iterations"]),
+            "learning_rate": float(cfg["learning_rate"]), "l2_leaf_reg": float(cfg.get("l2_leaf_reg", 3.0)),
+            "random_seed": int(cfg["random_seed"])}))
+        losses.append(loss)
+    np.savez_compressed(os.path.join(OUT, "ranking_corpus.npz"), **arrays)
+    return ["ranking_corpus/" + l for l in losses]
+
+
 def main():
     ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("CB_REFERENCE", "")
     if not ref or not os.path.isdir(ref):
@@ -242,6 +271,7 @@ def main():
     border_cells = border_fixtures(ref)
     written = e2e_fixtures(ref)
     written.append(multiclass_fixture(ref))
+    written += ranking_fixtures(ref)
     with open(os.path.join(OUT, "MANIFEST.json"), "w") as f:
         json.dump({"generator": "tests/golden/make_golden.py",
                    "origin": "upstream CatBoost 1.2.10 fixtures committed under the reference's "

@@ -1,0 +1,79 @@
+"""Pin the oracle's grouped-loss loop (QueryRMSE, PairLogit) to upstream.
+
+tests/golden/ranking_corpus.npz comes from the reference's frozen ranking
+corpus (crates/cb-oracle/fixtures/ranking_corpus: 12 objects in 5 contiguous
+groups, 7 explicit pairs, depth 2, 5 iterations, lr 0.3, Newton leaves), which
+the reference's own ranking oracle tests train against.  Trees are compared
+both with the full standalone GreedyLogSum border set (border_count 254) and
+with the model's own borders; leaf values and staged approximants at the
+reference's 1e-5 bar (crates/cb-oracle/src/compare.rs:46-148).
+"""
+import json
+import os
+
+import numpy as np
+import pytest
+
+from oracle import oracle
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "ranking_corpus.npz")
+TOL = 1e-5
+
+
+def _load():
+    z = np.load(GOLDEN)
+    return {k: z[k] for k in z.files}
+
+
+def _fit(d, loss, borders, **kw):
+    p = json.loads(str(d[f"{loss}__params"]))
+    bins = oracle.quantize(d["X"].T.copy(), borders)
+    args = dict(loss=loss, pairs=d["pairs"], depth=p["depth"], iterations=p["iterations"],
+                learning_rate=p["learning_rate"], l2_leaf_reg=p["l2_leaf_reg"], random_seed=p["random_seed"])
+    args.update(kw)
+    return oracle.train_ranking(bins, [len(b) for b in borders], d["y"], d["group_offsets"], **args)
+
+
+@pytest.mark.parametrize("loss", ["QueryRMSE", "PairLogit"])
+@pytest.mark.parametrize("border_set", ["full", "model"])
+def test_ranking_matches_upstream(loss, border_set):
+    d = _load()
+    X = d["X"]
+    sf, sv = d[f"{loss}__split_feature"], d[f"{loss}__split_border"]
+    if border_set == "full":
+        borders = [oracle.select_borders(X[:, f], 254, "GreedyLogSum", "Min") for f in range(X.shape[1])]
+    else:
+        borders = [np.unique(sv[sf == f]) for f in range(X.shape[1])]
+    fit = _fit(d, loss, borders)
+    np.testing.assert_array_equal(fit.split_feature, sf)
+    got = np.array([[borders[f][b] for f, b in zip(rf, rb)] for rf, rb in zip(fit.split_feature, fit.split_bin)])
+    np.testing.assert_array_equal(got.astype(np.float32), sv.astype(np.float32))
+    assert np.max(np.abs(fit.leaf_values - d[f"{loss}__leaf_values"])) <= TOL
+    assert np.max(np.abs(fit.staged - d[f"{loss}__staged"])) <= TOL
+
+
+def test_pairlogit_leaves_are_centred():
+    # normalize_leaf_values: the document-weighted mean of a PairLogit tree's
+    # (pre-learning-rate) leaf values is zero; QueryRMSE leaves are not centred
+    d = _load()
+    X = d["X"]
+    borders = [oracle.select_borders(X[:, f], 254, "GreedyLogSum", "Min") for f in range(X.shape[1])]
+    fit = _fit(d, "PairLogit", borders, iterations=3)
+    bins = oracle.quantize(X.T.copy(), borders)
+    for t in range(3):
+        leaf = np.zeros(X.shape[0], dtype=np.int64)
+        for l, (f, b) in enumerate(zip(fit.split_feature[t], fit.split_bin[t])):
+            leaf |= (bins[f].astype(np.int64) > b).astype(np.int64) << l
+        cnt = np.bincount(leaf, minlength=fit.leaf_values.shape[1])
+        assert abs(float(np.dot(fit.leaf_values[t], cnt))) < 1e-12
+        assert np.any(fit.raw_leaf_values[t] != 0)
+
+
+def test_group_offsets_validated():
+    d = _load()
+    X = d["X"]
+    borders = [oracle.select_borders(X[:, f], 8) for f in range(X.shape[1])]
+    bins = oracle.quantize(X.T.copy(), borders)
+    with pytest.raises(RuntimeError):
+        oracle.train_ranking(bins, [len(b) for b in borders], d["y"], np.array([0, 5]), loss="QueryRMSE", depth=2,
+                             iterations=1)
