@@ -9,7 +9,7 @@ from ._lib import CbGpuError, load as load_library  # noqa: F401
 from .runtime import (B200MultiRuntime, B200Runtime, DeviceGrownTree, DeviceTrainConfig, Derivatives,  # noqa: F401
                       apply_oblivious, bootstrap_weights, flatten_oblivious, histogram, nccl_unique_id,
                       select_borders)
-from .boosting import (FitParams, MultiClassModel, ObliviousModel, fit, fit_multiclass,  # noqa: F401
-                       seq_sum, starting_approx)
+from .boosting import (FitParams, MultiClassModel, ObliviousModel, RankingModel, fit,  # noqa: F401
+                       fit_multiclass, fit_ranking, normalize_leaf_values, seq_sum, starting_approx)
 
 __version__ = "0.1.0"

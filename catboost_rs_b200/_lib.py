@@ -38,6 +38,7 @@ EXPORTS = [
     "cbgpu_session_mark", "cbgpu_session_elapsed_ms", "cbgpu_histogram_noalloc",
     "cbgpu_select_borders", "cbgpu_apply_oblivious",
     "cbgpu_multi_begin_raw", "cbgpu_multi_grow_tree", "cbgpu_multi_approx", "cbgpu_multi_end",
+    "cbgpu_rank_begin_raw",
 ]
 
 _lib = None
@@ -85,6 +86,7 @@ def load(path: str = LIB_PATH):
         "cbgpu_multi_begin_raw": ([C.POINTER(BeginArgs), i32, vp, vp, vp, C.POINTER(vp)], C.c_int),
         "cbgpu_multi_grow_tree": ([vp, vp, vp, i64, vp, i64, vp, vp, vp, vp, vp, i32], C.c_int),
         "cbgpu_multi_approx": ([vp, vp, i64], C.c_int),
+        "cbgpu_rank_begin_raw": ([C.POINTER(BeginArgs), vp, i32, vp, vp, i64, vp, vp, vp, C.POINTER(vp)], C.c_int),
         "cbgpu_multi_end": ([vp], C.c_int),
         "cbgpu_nccl_unique_id": ([vp], C.c_int),
         "cbgpu_version": ([], C.c_char_p),

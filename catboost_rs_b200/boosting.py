@@ -197,3 +197,79 @@ def fit_multiclass(float_columns: Sequence[np.ndarray], borders: Sequence[Sequen
     finally:
         rt.end_device_training()
     return MultiClassModel([np.asarray(b, dtype=np.float64) for b in borders], sf, sb, lv, st)
+
+
+@dataclass
+class RankingModel:
+    """Per-tree splits and the normalised, learning-rate scaled leaf values
+    [T, 2^depth] of a grouped-loss fit, plus the raw Newton deltas the seam
+    returned and optionally the staged approximants [T, n]."""
+    borders: list
+    split_feature: np.ndarray
+    split_bin: np.ndarray
+    leaf_values: np.ndarray
+    raw_leaf_values: np.ndarray
+    staged: Optional[np.ndarray] = None
+
+    def split_borders(self) -> np.ndarray:
+        return np.array([[self.borders[f][b] for f, b in zip(rf, rb)]
+                         for rf, rb in zip(self.split_feature, self.split_bin)])
+
+
+def normalize_leaf_values(pairwise: bool, lr: float, leaf_weights, raw) -> np.ndarray:
+    """cb-train's normalize_leaf_values (boosting.rs:2844-2880): pairwise losses
+    subtract the document-weighted mean leaf value (empty leaves become 0),
+    then every value is scaled by the learning rate."""
+    v = np.array(raw, dtype=np.float64)
+    if pairwise:
+        total = seq_sum(leaf_weights)
+        if abs(total) > 1e-9:
+            avg = seq_sum(v * leaf_weights) / total
+            v = np.where(np.abs(leaf_weights) > 1e-9, v - avg, 0.0)
+    return v * lr
+
+
+def fit_ranking(float_columns: Sequence[np.ndarray], borders: Sequence[Sequence[float]], target, group_offsets,
+                params: FitParams, pairs=None, weights=None, *, staged: bool = False,
+                device: int = 0) -> RankingModel:
+    """QueryRMSE / PairLogit fit (params.loss) on raw f32 columns with fixed
+    borders: cb-train's grouped loop (pointwise histograms, Newton leaves)
+    over the device's ranking arm; leaf normalisation on the host as cb-train
+    does it."""
+    p = params
+    cols = [np.ascontiguousarray(c, dtype=np.float32) for c in float_columns]
+    F = len(cols)
+    n = cols[0].size if F else 0
+    y = np.ascontiguousarray(target, dtype=np.float64)
+    w = None if weights is None else np.ascontiguousarray(weights, dtype=np.float64)
+    sw = seq_sum(w) if w is not None else float(n)
+    scaled_l2 = p.l2_leaf_reg * (sw / n) if n else p.l2_leaf_reg
+    lr = float(np.float32(p.learning_rate))  # boosting.rs:4958
+    cfg = DeviceTrainConfig(bootstrap_type="No", rng_seed=p.random_seed, bias=0.0, device=device)
+    rt = B200MultiRuntime()
+    n_bins = max(len(b) for b in borders) + 1
+    ok = rt.begin_ranking_raw(p.loss, p.depth, True, 1, p.score_function, cols, borders, w, n, F, n_bins, lr,
+                              scaled_l2, cfg, group_offsets, pairs)
+    if not ok:
+        raise RuntimeError(f"device declined: {rt.decline_reason}")
+    T, D = p.iterations, p.depth
+    L = 1 << D
+    sf = np.zeros((T, D), dtype=np.int32)
+    sb = np.zeros((T, D), dtype=np.int32)
+    lv = np.zeros((T, L), dtype=np.float64)
+    raw = np.zeros((T, L), dtype=np.float64)
+    st = np.zeros((T, n), dtype=np.float64) if staged else None
+    doc_w = w if w is not None else np.ones(n)
+    try:
+        for it in range(T):
+            tree = rt.grow_tree_on_device(None, y, [], leaf_of_bytes=2, resident_approx=True)
+            for l, (f, b, _) in enumerate(tree.splits):
+                sf[it, l], sb[it, l] = f, b
+            raw[it] = tree.leaf_values
+            leaf_w = np.bincount(tree.leaf_of.astype(np.int64), weights=doc_w, minlength=L)
+            lv[it] = normalize_leaf_values(p.loss == "PairLogit", lr, leaf_w, tree.leaf_values)
+            if staged:
+                st[it] = rt.resident_approx()[0]
+    finally:
+        rt.end_device_training()
+    return RankingModel([np.asarray(b, dtype=np.float64) for b in borders], sf, sb, lv, raw, st)

@@ -28,6 +28,13 @@
 // rounding of each value (2^-40 of the largest value or finer).  The host keeps
 // the main TFastRng64 stream replica with cb-train's draw accounting, as the
 // scalar session does.  One GPU per session; MVS and document sharding decline.
+//
+// The same session serves the grouped (ranking) losses QueryRMSE and PairLogit
+// at K = 1 (cbgpu_rank_begin_raw): rk_der_kernel computes the grouped ders one
+// thread per group in the reference's order, the histogram weight channel is
+// PairLogit's pairwise weights, and rk_leafsum / rk_newton give the Newton
+// leaves and the PairLogit leaf centring.
+#include <algorithm>
 #include <cfloat>
 #include <cmath>
 #include <cstdarg>
@@ -105,7 +112,8 @@ struct McState {
     uint32_t pad;
     unsigned long long maxbits;  // bit pattern of max |score channel| (a non-negative double)
     int32_t hist_shift;          // score channels are llrint(v * 2^hist_shift)
-    int32_t pad2;
+    int32_t leaf_shift;          // ranking mode: leaf sums are llrint(v * 2^leaf_shift)
+    unsigned long long lmaxbits; // ranking mode: max |der1|, |der2|, |w| bit pattern
 };
 
 // ---- kernels ---------------------------------------------------------------
@@ -476,6 +484,152 @@ __global__ void mc_apply_pending_kernel(int64_t n, int K, int L, double* __restr
     }
 }
 
+// ---- ranking mode (grouped losses, K = 1) ----------------------------------
+
+enum : int { kRankQueryRmse = 0, kRankPairLogit = 1 };
+
+// Grouped derivatives (calc_ders_for_queries, crates/cb-compute/src/
+// ranking_der.rs:139-440), one thread per group in the reference's order, so
+// every f64 sum rounds as the CPU's does:
+//  QueryRMSE  queryAvrg = sum((t - a) * w) / sum(w); der1 = ((t - a) - queryAvrg) * w,
+//             der2 = -1 * w;
+//  PairLogit  doc-ascending winners, competitor order: p = e^l / (e^l + e^w),
+//             winner += p, loser -= p (der2: p * (p - 1)), pair weight 1.
+// The ders carry the weights already (boosting.rs:7453-7490).
+__global__ void rk_der_kernel(int n_groups, int mode, const int64_t* __restrict__ goff,
+                              const int64_t* __restrict__ cstart, const int64_t* __restrict__ closer,
+                              const double* __restrict__ approx, const double* __restrict__ target,
+                              const double* __restrict__ weight, double* __restrict__ d1, double* __restrict__ d2,
+                              McState* __restrict__ ms) {
+    const int g = blockIdx.x * blockDim.x + threadIdx.x;
+    if (g >= n_groups) return;
+    const int64_t b = goff[g], e = goff[g + 1];
+    bool finite = true;
+    if (mode == kRankQueryRmse) {
+        double num = 0.0, den = 0.0;
+        for (int64_t i = b; i < e; ++i) {
+            const double w = weight ? weight[i] : 1.0;
+            num = __dadd_rn(num, __dmul_rn(__dsub_rn(target[i], approx[i]), w));
+        }
+        for (int64_t i = b; i < e; ++i) den = __dadd_rn(den, weight ? weight[i] : 1.0);
+        const double avg = den > 0.0 ? __ddiv_rn(num, den) : 0.0;
+        for (int64_t i = b; i < e; ++i) {
+            const double w = weight ? weight[i] : 1.0;
+            d1[i] = __dmul_rn(__dsub_rn(__dsub_rn(target[i], approx[i]), avg), w);
+            d2[i] = __dmul_rn(-1.0, w);
+            finite &= isfinite(d1[i]);
+        }
+    } else {
+        for (int64_t i = b; i < e; ++i) {
+            d1[i] = 0.0;
+            d2[i] = 0.0;
+        }
+        for (int64_t wi = b; wi < e; ++wi) {
+            double wd = 0.0, wd2 = 0.0;
+            const double aw = approx[wi];
+            for (int64_t k = cstart[wi]; k < cstart[wi + 1]; ++k) {
+                const int64_t li = closer[k];
+                const double el = exp(approx[li]), ew = exp(aw);
+                const double den = __dadd_rn(el, ew);
+                const double p = den > 0.0 ? __ddiv_rn(el, den) : 0.5;
+                const double t = __dmul_rn(__dmul_rn(1.0, p), __dsub_rn(p, 1.0));
+                wd = __dadd_rn(wd, __dmul_rn(1.0, p));
+                wd2 = __dadd_rn(wd2, t);
+                d1[li] = __dsub_rn(d1[li], __dmul_rn(1.0, p));
+                d2[li] = __dadd_rn(d2[li], t);
+            }
+            d1[wi] = __dadd_rn(d1[wi], wd);
+            d2[wi] = __dadd_rn(d2[wi], wd2);
+        }
+        for (int64_t i = b; i < e; ++i) finite &= isfinite(d1[i]) && isfinite(d2[i]);
+    }
+    if (!finite) atomicOr(&ms->err, kMcErrNonFinite);
+}
+
+// max |der1|, |der2|, |w| of the tree -> leaf_shift (sums over n rows < 2^62)
+__global__ void rk_leafmax_kernel(int64_t n, const double* __restrict__ d1, const double* __restrict__ d2,
+                                  const double* __restrict__ weight, McState* __restrict__ ms) {
+    double mx = 0.0;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        mx = fmax(mx, fmax(fabs(d1[i]), fmax(fabs(d2[i]), fabs(weight ? weight[i] : 1.0))));
+    for (int o = 16; o > 0; o >>= 1) mx = fmax(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((threadIdx.x & 31) == 0 && mx > 0.0) atomicMax(&ms->lmaxbits, (unsigned long long)__double_as_longlong(mx));
+}
+
+__global__ void rk_leafshift_kernel(int64_t n, McState* ms) {
+    const double mx = __longlong_as_double((long long)ms->lmaxbits);
+    int e = 0;
+    if (mx > 0.0) frexp(mx, &e);
+    int t = 0;
+    while (t < 62 && (1ll << t) < n) ++t;
+    int sh = 61 - e - t;
+    if (sh > 1000) sh = 1000;
+    ms->leaf_shift = sh;
+}
+
+// Per-leaf int64 sums of der1, der2 (unit leaf weights for Newton,
+// boosting.rs:8345-8380) and the object weight (normalize_leaf_values' leaf
+// weights, boosting.rs:8525-8540): sums[leaf][3].
+__global__ void rk_leafsum_kernel(int64_t n, int L, const double* __restrict__ d1, const double* __restrict__ d2,
+                                  const double* __restrict__ weight, const uint16_t* __restrict__ leaf,
+                                  unsigned long long* __restrict__ sums, McState* __restrict__ ms) {
+    __shared__ unsigned long long t3[3 * (1 << kMcMaxDepth)];
+    for (int k = threadIdx.x; k < 3 * L; k += blockDim.x) t3[k] = 0ull;
+    __syncthreads();
+    const int sh = ms->leaf_shift;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int q = leaf[i];
+        if (q >= L) {
+            atomicOr(&ms->err, kMcErrLeafRange);
+            continue;
+        }
+        atomicAdd(&t3[3 * q], (unsigned long long)llrint(ldexp(d1[i], sh)));
+        atomicAdd(&t3[3 * q + 1], (unsigned long long)llrint(ldexp(d2[i], sh)));
+        atomicAdd(&t3[3 * q + 2], (unsigned long long)llrint(ldexp(weight ? weight[i] : 1.0, sh)));
+    }
+    __syncthreads();
+    for (int k = threadIdx.x; k < 3 * L; k += blockDim.x)
+        if (t3[k]) atomicAdd(&sums[k], t3[k]);
+}
+
+// Newton leaves sum(der1) / (-sum(der2) + scaled_l2) (leaf.rs:223-232); the
+// raw deltas go back through the seam; the approximant gets
+// normalize_leaf_values' result (PairLogit: minus the document-weighted mean,
+// boosting.rs:2844-2880) x lr.  One thread: L <= 1024 leaves.
+__global__ void rk_newton_kernel(int L, int pairwise, const unsigned long long* __restrict__ sums,
+                                 const McState* __restrict__ ms, double l2, double lr, double* __restrict__ leaf_raw,
+                                 double* __restrict__ leaf_lrv) {
+    if (blockIdx.x != 0 || threadIdx.x != 0) return;
+    const double inv = ldexp(1.0, -ms->leaf_shift);
+    for (int q = 0; q < L; ++q) {
+        const double s1 = __dmul_rn((double)(long long)sums[3 * q], inv);
+        const double s2 = __dmul_rn((double)(long long)sums[3 * q + 1], inv);
+        const double den = __dadd_rn(-s2, l2);
+        leaf_raw[q] = den == 0.0 ? 0.0 : __ddiv_rn(s1, den);
+    }
+    double avg = 0.0;
+    bool centre = false;
+    if (pairwise) {
+        double total = 0.0;
+        for (int q = 0; q < L; ++q) total = __dadd_rn(total, __dmul_rn((double)(long long)sums[3 * q + 2], inv));
+        if (fabs(total) > 1e-9) {
+            double acc = 0.0;
+            for (int q = 0; q < L; ++q)
+                acc = __dadd_rn(acc, __dmul_rn(leaf_raw[q], __dmul_rn((double)(long long)sums[3 * q + 2], inv)));
+            avg = __ddiv_rn(acc, total);
+            centre = true;
+        }
+    }
+    for (int q = 0; q < L; ++q) {
+        double v = leaf_raw[q];
+        if (centre) {
+            const double w = __dmul_rn((double)(long long)sums[3 * q + 2], inv);
+            v = fabs(w) > 1e-9 ? __dsub_rn(v, avg) : 0.0;
+        }
+        leaf_lrv[q] = __dmul_rn(v, lr);
+    }
+}
+
 unsigned grid_for(int64_t n, int threads = kMcThreads) {
     int64_t b = (n + threads - 1) / threads;
     if (b > 148 * 16) b = 148 * 16;
@@ -508,9 +662,20 @@ struct cbgpu_multi_session {
     double* h_raw = nullptr;
     void* leaf_export = nullptr;
     size_t hist_cells = 0;
+    // ranking mode (grouped losses, K = 1)
+    int rank_mode = -1;  // -1: MultiClass; kRankQueryRmse / kRankPairLogit
+    int n_groups = 0;
+    int64_t *d_goff = nullptr, *d_cstart = nullptr, *d_closer = nullptr;
+    double *d_eff = nullptr, *d_der2 = nullptr, *d_tgt = nullptr;
 
     ~cbgpu_multi_session() {
         if (st) cudaStreamSynchronize(st);
+        cudaFree(d_goff);
+        cudaFree(d_cstart);
+        cudaFree(d_closer);
+        cudaFree(d_eff);
+        cudaFree(d_der2);
+        cudaFree(d_tgt);
         cudaFree(bins_fm);
         cudaFree(d_bc);
         cudaFree(approx);
@@ -596,7 +761,7 @@ int begin_impl(const cbgpu_begin_args* a, int32_t K, const float* const* cols, c
     s->hist_cells = (size_t)(L / 2) * F * s->NB * C;  // the deepest level has L/2 parents
     MDA(s->hist, s->hist_cells);
     MDA(s->scores, (size_t)F * s->NB);
-    MDA(s->sums, (size_t)L * (K + pk));
+    MDA(s->sums, (size_t)L * std::max(K + pk, 3));  // the ranking mode keeps 3 sums per leaf
     MDA(s->leaf_raw, (size_t)L * K);
     MDA(s->leaf_lrv, (size_t)L * K);
     MDA(s->d_ms, 1);
@@ -708,6 +873,110 @@ int cbgpu_multi_begin_raw(const cbgpu_begin_args* a, int32_t approx_dim, const f
     return CBGPU_OK;
 }
 
+int cbgpu_rank_begin_raw(const cbgpu_begin_args* a, const int64_t* group_offsets, int32_t n_groups,
+                         const int64_t* pair_winner, const int64_t* pair_loser, int64_t n_pairs,
+                         const float* const* float_columns, const double* borders_flat, const int32_t* border_counts,
+                         cbgpu_multi_session** out) {
+    if (!out) return mfail(CBGPU_ERR_INVALID, "rank_begin: out is NULL");
+    *out = nullptr;
+    if (!a || !border_counts || !group_offsets || (a->n > 0 && !float_columns) ||
+        (n_pairs > 0 && (!pair_winner || !pair_loser)) || n_pairs < 0)
+        return mfail(CBGPU_ERR_INVALID, "rank_begin: bad arguments");
+    int mode;
+    if (a->loss == CBGPU_LOSS_QUERYRMSE) mode = kRankQueryRmse;
+    else if (a->loss == CBGPU_LOSS_PAIRLOGIT) mode = kRankPairLogit;
+    else return mfail(CBGPU_DECLINED, "rank_begin: loss %d is not QueryRMSE / PairLogit", a->loss);
+    if (a->grow_policy != CBGPU_GROW_SYMMETRIC || !a->boosting_type_is_plain || a->fold_count != 1)
+        return mfail(CBGPU_DECLINED, "rank_begin: only Plain SymmetricTree with one fold");
+    if (a->score_function != CBGPU_SCORE_COSINE && a->score_function != CBGPU_SCORE_L2)
+        return mfail(CBGPU_DECLINED, "rank_begin: score function not covered");
+    if (a->random_strength != 0.0 || a->bootstrap_type != CBGPU_BOOT_NO || a->sample_from_host)
+        return mfail(CBGPU_DECLINED, "rank_begin: bootstrap / random_strength not covered on this arm");
+    if (a->world_size != 1) return mfail(CBGPU_DECLINED, "rank_begin: one GPU per ranking session");
+    if (a->depth < 1 || a->depth > kMcMaxDepth)
+        return mfail(CBGPU_DECLINED, "rank_begin: depth %d outside 1..%d", a->depth, kMcMaxDepth);
+    const int64_t n = a->n;
+    if (n < 1 || n > (int64_t)65535 * kMcChunk || a->n_features < 1)
+        return mfail(CBGPU_ERR_INVALID, "rank_begin: bad n / n_features");
+    for (int f = 0; f < a->n_features; ++f)
+        if (border_counts[f] < 0 || border_counts[f] > 255)
+            return mfail(CBGPU_DECLINED, "rank_begin: feature %d has %d borders (> 255)", f, border_counts[f]);
+    {
+        int64_t off = 0;
+        for (int f = 0; f < a->n_features; ++f) {
+            for (int k = 1; k < border_counts[f]; ++k)
+                if (!(borders_flat[off + k - 1] < borders_flat[off + k]))
+                    return mfail(CBGPU_ERR_INVALID, "rank_begin: borders of feature %d are not ascending", f);
+            off += border_counts[f];
+        }
+    }
+    // contiguous groups over object order (query.h:48-67)
+    if (n_groups < 1 || group_offsets[0] != 0 || group_offsets[n_groups] != n)
+        return mfail(CBGPU_ERR_INVALID, "rank_begin: group offsets must run from 0 to n");
+    std::vector<int32_t> group_of((size_t)n);
+    for (int g = 0; g < n_groups; ++g) {
+        if (group_offsets[g + 1] < group_offsets[g])
+            return mfail(CBGPU_ERR_INVALID, "rank_begin: group offsets decrease at group %d", g);
+        for (int64_t i = group_offsets[g]; i < group_offsets[g + 1]; ++i) group_of[(size_t)i] = g;
+    }
+    // competitors (query_info.rs:205-250): pairs in input order on their
+    // winner's row, weight 1; the pairwise weights count the incident pairs
+    // (calc_pairwise_weights, boosting.rs:1761-1780)
+    std::vector<int64_t> cstart((size_t)n + 1, 0), closer((size_t)std::max<int64_t>(n_pairs, 1));
+    std::vector<double> eff((size_t)n, 0.0);
+    if (mode == kRankPairLogit) {
+        for (int64_t k = 0; k < n_pairs; ++k) {
+            const int64_t wv = pair_winner[k], lv = pair_loser[k];
+            if (wv < 0 || wv >= n || lv < 0 || lv >= n || group_of[(size_t)wv] != group_of[(size_t)lv])
+                return mfail(CBGPU_ERR_INVALID, "rank_begin: pair (%lld, %lld) is out of range or crosses group "
+                                                "boundaries", (long long)wv, (long long)lv);
+            cstart[(size_t)wv + 1]++;
+        }
+        for (int64_t i = 0; i < n; ++i) cstart[(size_t)i + 1] += cstart[(size_t)i];
+        std::vector<int64_t> fill(cstart.begin(), cstart.end() - 1);
+        for (int64_t k = 0; k < n_pairs; ++k) closer[(size_t)fill[(size_t)pair_winner[k]]++] = pair_loser[k];
+        for (int g = 0; g < n_groups; ++g)
+            for (int64_t wi = group_offsets[g]; wi < group_offsets[g + 1]; ++wi)
+                for (int64_t k = cstart[(size_t)wi]; k < cstart[(size_t)wi + 1]; ++k) {
+                    eff[(size_t)wi] += 1.0;
+                    eff[(size_t)closer[(size_t)k]] += 1.0;
+                }
+    } else {
+        for (int64_t i = 0; i < n; ++i) eff[(size_t)i] = a->weight ? a->weight[i] : 1.0;
+    }
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) return mfail(CBGPU_ERR_NO_DEVICE, "no CUDA device");
+    if (a->device < 0 || a->device >= ndev) return mfail(CBGPU_ERR_INVALID, "rank_begin: bad device");
+    auto* s = new cbgpu_multi_session();
+    int rc = begin_impl(a, 1, float_columns, borders_flat, border_counts, s);
+    if (!rc) {
+        s->rank_mode = mode;
+        s->n_groups = n_groups;
+        rc = mdalloc(&s->d_goff, (size_t)n_groups + 1);
+        if (!rc) rc = mdalloc(&s->d_cstart, (size_t)n + 1);
+        if (!rc) rc = mdalloc(&s->d_closer, closer.size());
+        if (!rc) rc = mdalloc(&s->d_eff, (size_t)n);
+        if (!rc) rc = mdalloc(&s->d_der2, (size_t)n);
+        if (!rc) rc = mdalloc(&s->d_tgt, (size_t)n);
+    }
+    if (!rc) {
+        cudaError_t e = cudaMemcpy(s->d_goff, group_offsets, sizeof(int64_t) * ((size_t)n_groups + 1),
+                                   cudaMemcpyHostToDevice);
+        if (e == cudaSuccess)
+            e = cudaMemcpy(s->d_cstart, cstart.data(), sizeof(int64_t) * cstart.size(), cudaMemcpyHostToDevice);
+        if (e == cudaSuccess)
+            e = cudaMemcpy(s->d_closer, closer.data(), sizeof(int64_t) * closer.size(), cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = cudaMemcpy(s->d_eff, eff.data(), sizeof(double) * (size_t)n, cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) rc = mfail(CBGPU_ERR_CUDA, "rank_begin: upload failed: %s", cudaGetErrorString(e));
+    }
+    if (rc) {
+        delete s;
+        return rc;
+    }
+    *out = s;
+    return CBGPU_OK;
+}
+
 int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const double* target, int64_t n,
                           const double* sample, int64_t sample_len, int32_t* split_feature, int32_t* split_bin,
                           int32_t* n_splits, double* leaf_values, void* leaf_of, int32_t leaf_of_bytes) {
@@ -726,6 +995,12 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
     const int pk = K * (K + 1) / 2;
     cudaStream_t st = s->st;
     MCU(cudaSetDevice(s->device));
+    if (!s->target_ready && s->rank_mode >= 0) {
+        if (!target) return mfail(CBGPU_ERR_INVALID, "multi_grow: the first call needs the target");
+        MCU(cudaMemcpyAsync(s->d_tgt, target, sizeof(double) * n, cudaMemcpyHostToDevice, st));
+        MCU(cudaStreamSynchronize(st));
+        s->target_ready = true;
+    }
     if (!s->target_ready) {
         if (!target) return mfail(CBGPU_ERR_INVALID, "multi_grow: the first call needs the target");
         std::vector<int32_t> cls((size_t)n);
@@ -768,16 +1043,26 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
     MCU(cudaMemcpyAsync(s->d_tp, s->h_tp, sizeof(TreeParams), cudaMemcpyHostToDevice, st));
     MCU(cudaMemsetAsync(s->d_ms, 0, sizeof(McState), st));
     const unsigned g = grid_for(n);
-    mc_der_kernel<<<g, kMcThreads, 0, st>>>(n, K, s->approx, s->target, s->weight, s->leaf, s->leaf_lrv, L,
-                                            s->pending ? 1 : 0, s->wd1, s->d_ms);
+    if (s->rank_mode >= 0) {
+        if (s->pending)
+            mc_apply_pending_kernel<<<g, kMcThreads, 0, st>>>(n, 1, L, s->approx, s->leaf, s->leaf_lrv);
+        rk_der_kernel<<<(unsigned)((s->n_groups + 127) / 128), 128, 0, st>>>(
+            s->n_groups, s->rank_mode, s->d_goff, s->d_cstart, s->d_closer, s->approx, s->d_tgt, s->weight, s->wd1,
+            s->d_der2, s->d_ms);
+    } else {
+        mc_der_kernel<<<g, kMcThreads, 0, st>>>(n, K, s->approx, s->target, s->weight, s->leaf, s->leaf_lrv, L,
+                                                s->pending ? 1 : 0, s->wd1, s->d_ms);
+    }
     MCU(cudaGetLastError());
     s->pending = false;
     // the previous tree's leaf ids are consumed: every row starts this tree in leaf 0
     MCU(cudaMemsetAsync(s->leaf, 0, sizeof(uint16_t) * (size_t)n, st));
     if (boot_mode) launch_bootstrap(boot_mode, n, 0, s->d_tp, (double)s->sample_rate, s->temp, s->sw32, st);
-    mc_max_kernel<<<g, kMcThreads, 0, st>>>(n, K, s->wd1, s->weight, s_mode, s->sw32, s->sw64, s->d_ms);
+    // the histogram weight channel: PairLogit's pairwise weights, else the object weights
+    const double* hw = s->rank_mode >= 0 ? s->d_eff : s->weight;
+    mc_max_kernel<<<g, kMcThreads, 0, st>>>(n, K, s->wd1, hw, s_mode, s->sw32, s->sw64, s->d_ms);
     mc_shift_kernel<<<1, 1, 0, st>>>(n, s->d_ms);
-    mc_pack_kernel<<<g, kMcThreads, 0, st>>>(n, K, s->wd1, s->weight, s_mode, s->sw32, s->sw64, s->d_ms, s->q);
+    mc_pack_kernel<<<g, kMcThreads, 0, st>>>(n, K, s->wd1, hw, s_mode, s->sw32, s->sw64, s->d_ms, s->q);
     MCU(cudaGetLastError());
     const unsigned chunks = (unsigned)((n + kMcChunk - 1) / kMcChunk);
     for (int l = 0; l < D; ++l) {
@@ -798,17 +1083,28 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
         mc_route_kernel<<<g, kMcThreads, 0, st>>>(n, l, s->bins_fm, s->d_ms, s->leaf);
         MCU(cudaGetLastError());
     }
-    // leaf values from the unsampled channels (boosting.rs:2610-2700)
-    const size_t ltab = (size_t)L * (K + pk) * sizeof(unsigned long long);
-    const int luse = ltab <= kMcSmemTable ? 1 : 0;
-    MCU(cudaMemsetAsync(s->sums, 0, ltab, st));
-    if (luse && ltab > 48 * 1024)
-        MCU(cudaFuncSetAttribute(mc_leafsum_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ltab));
-    mc_leafsum_kernel<<<g, kMcThreads, luse ? ltab : 0, st>>>(n, K, L, s->approx, s->wd1, s->weight, s->leaf,
-                                                             s->leaf_shift, s->sums, luse, s->d_ms);
-    mc_newton_kernel<<<(L + 63) / 64, 64, 0, st>>>(K, L, s->sums, s->leaf_shift, s->l2, s->lr, s->leaf_raw,
-                                                   s->leaf_lrv);
-    MCU(cudaGetLastError());
+    if (s->rank_mode >= 0) {
+        // Newton leaves over the grouped ders, then normalize_leaf_values
+        rk_leafmax_kernel<<<g, kMcThreads, 0, st>>>(n, s->wd1, s->d_der2, s->weight, s->d_ms);
+        rk_leafshift_kernel<<<1, 1, 0, st>>>(n, s->d_ms);
+        MCU(cudaMemsetAsync(s->sums, 0, sizeof(unsigned long long) * 3 * (size_t)L, st));
+        rk_leafsum_kernel<<<g, kMcThreads, 0, st>>>(n, L, s->wd1, s->d_der2, s->weight, s->leaf, s->sums, s->d_ms);
+        rk_newton_kernel<<<1, 1, 0, st>>>(L, s->rank_mode == kRankPairLogit ? 1 : 0, s->sums, s->d_ms, s->l2, s->lr,
+                                          s->leaf_raw, s->leaf_lrv);
+        MCU(cudaGetLastError());
+    } else {
+        // leaf values from the unsampled channels (boosting.rs:2610-2700)
+        const size_t ltab = (size_t)L * (K + pk) * sizeof(unsigned long long);
+        const int luse = ltab <= kMcSmemTable ? 1 : 0;
+        MCU(cudaMemsetAsync(s->sums, 0, ltab, st));
+        if (luse && ltab > 48 * 1024)
+            MCU(cudaFuncSetAttribute(mc_leafsum_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ltab));
+        mc_leafsum_kernel<<<g, kMcThreads, luse ? ltab : 0, st>>>(n, K, L, s->approx, s->wd1, s->weight, s->leaf,
+                                                                 s->leaf_shift, s->sums, luse, s->d_ms);
+        mc_newton_kernel<<<(L + 63) / 64, 64, 0, st>>>(K, L, s->sums, s->leaf_shift, s->l2, s->lr, s->leaf_raw,
+                                                       s->leaf_lrv);
+        MCU(cudaGetLastError());
+    }
     MCU(cudaMemcpyAsync(s->h_raw, s->leaf_raw, sizeof(double) * (size_t)L * K, cudaMemcpyDeviceToHost, st));
     MCU(cudaMemcpyAsync(s->h_ms, s->d_ms, sizeof(McState), cudaMemcpyDeviceToHost, st));
     if (leaf_of && leaf_of_bytes) {

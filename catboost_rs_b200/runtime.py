@@ -18,7 +18,7 @@ import numpy as np
 
 from . import _lib
 
-LOSS = {"RMSE": 0, "Rmse": 0, "Logloss": 1, "CrossEntropy": 2, "MultiClass": 3}
+LOSS = {"RMSE": 0, "Rmse": 0, "Logloss": 1, "CrossEntropy": 2, "MultiClass": 3, "QueryRMSE": 4, "PairLogit": 5}
 SCORE = {"Cosine": 0, "L2": 1, "SolarL2": 2, "NewtonL2": 3, "NewtonCosine": 4, "LOOL2": 5, "SatL2": 6}
 BOOT = {"No": 0, "Bayesian": 1, "Bernoulli": 2, "MVS": 3, "Mvs": 3, "Poisson": 4}
 GROW = {"SymmetricTree": 0, "Depthwise": 1, "Lossguide": 2, "Region": 3}
@@ -314,6 +314,35 @@ class B200MultiRuntime(B200Runtime):
     def begin_device_training(self, *args, **kwargs) -> bool:
         raise _lib.CbGpuError(_lib.DECLINED, "the multi-output arm quantizes on the device (begin_raw)")
 
+    def begin_ranking_raw(self, loss, depth, boosting_type_is_plain, fold_count, score_function, float_columns,
+                          feature_borders, weight, n, n_features, n_bins, learning_rate, scaled_l2,
+                          config: DeviceTrainConfig, group_offsets, pairs=None) -> bool:
+        """The grouped families (FamilyTreeArgs::Ranking / ::Pairwise) for
+        QueryRMSE / PairLogit: group offsets [n_groups + 1] and, for PairLogit,
+        (winner, loser) global object ids; grown with grow_tree_on_device
+        (family None, approx_dim 1)."""
+        self.end_device_training()
+        cols = [np.ascontiguousarray(c, dtype=np.float32) for c in float_columns]
+        if len(cols) != n_features or any(c.size != n for c in cols):
+            raise _lib.CbGpuError(_lib.ERR_INVALID, "LengthMismatch: float_columns")
+        counts = np.array([len(b) for b in feature_borders], dtype=np.int32)
+        flat = np.ascontiguousarray(
+            np.concatenate([np.asarray(b, dtype=np.float64) for b in feature_borders])
+            if counts.sum() else np.zeros(1), dtype=np.float64)
+        colptrs = (C.c_void_p * max(1, len(cols)))(*[c.ctypes.data for c in cols])
+        go = np.ascontiguousarray(group_offsets, dtype=np.int64)
+        pr = np.zeros((0, 2), dtype=np.int64) if pairs is None else np.asarray(pairs, dtype=np.int64).reshape(-1, 2)
+        pw = np.ascontiguousarray(pr[:, 0])
+        pl = np.ascontiguousarray(pr[:, 1])
+        a = self._args(loss, depth, boosting_type_is_plain, fold_count, score_function, weight, n,
+                       n_features, n_bins, learning_rate, scaled_l2, config)
+        self._keep += [go, pw, pl]
+        rc = self._L.cbgpu_rank_begin_raw(C.byref(a), _ptr(go), go.size - 1, _ptr(pw), _ptr(pl), pw.size, colptrs,
+                                          _ptr(flat), _ptr(counts), C.byref(self._s))
+        ok = self._finish_begin(rc, n, depth)
+        self.approx_dim = 1 if ok else 0
+        return ok
+
     def grow_tree_on_device(self, approx, target, sample, family=None, leaf_of_bytes: int = 4,
                             resident_approx: bool = False) -> Optional[DeviceGrownTree]:
         """family = ("MultiOutput", approx_k, approx_dim); approx_k None with
@@ -322,6 +351,10 @@ class B200MultiRuntime(B200Runtime):
             return None
         K, n, D = self.approx_dim, self.n, self.depth
         ak = None
+        if family is None and not resident_approx and approx is not None and K == 1:
+            ak = np.ascontiguousarray(approx, dtype=np.float64).reshape(-1)  # the grouped families (K = 1)
+            if ak.size != n:
+                raise _lib.CbGpuError(_lib.ERR_INVALID, f"LengthMismatch: approx has {ak.size}, expected {n}")
         if family is not None:
             kind, fam_approx, fam_dim = family
             if kind != "MultiOutput" or int(fam_dim) != K:

@@ -45,10 +45,12 @@ typedef enum {
 } cbgpu_status;
 
 /* Loss (runtime.rs:57-70): only the device-covered subset.  MultiClass is
- * served by the multi-output session (cbgpu_multi_begin_raw); the scalar
- * session declines it. */
+ * served by the multi-output session (cbgpu_multi_begin_raw), QueryRMSE and
+ * PairLogit by its ranking mode (cbgpu_rank_begin_raw); the scalar session
+ * declines them. */
 typedef enum {
-    CBGPU_LOSS_RMSE = 0, CBGPU_LOSS_LOGLOSS = 1, CBGPU_LOSS_CROSSENTROPY = 2, CBGPU_LOSS_MULTICLASS = 3
+    CBGPU_LOSS_RMSE = 0, CBGPU_LOSS_LOGLOSS = 1, CBGPU_LOSS_CROSSENTROPY = 2, CBGPU_LOSS_MULTICLASS = 3,
+    CBGPU_LOSS_QUERYRMSE = 4, CBGPU_LOSS_PAIRLOGIT = 5
 } cbgpu_loss;
 
 /* EScoreFunction (runtime.rs:834-864); Cosine is the default. */
@@ -277,6 +279,26 @@ CBGPU_API int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx
                                     int64_t n, const double* sample, int64_t sample_len, int32_t* split_feature,
                                     int32_t* split_bin, int32_t* n_splits, double* leaf_values, void* leaf_of,
                                     int32_t leaf_of_bytes);
+
+/* The seam's grouped families (FamilyTreeArgs::Ranking / ::Pairwise,
+ * runtime.rs:918-934) for QueryRMSE and PairLogit on pointwise histograms:
+ * the reference's device session declines them
+ * (crates/cb-backend/src/gpu_runtime/session.rs:1401-1444); this mode
+ * reproduces cb-train's grouped CPU branch (grouped ders,
+ * crates/cb-compute/src/ranking_der.rs:139-440; PairLogit's pairwise
+ * histogram weights, boosting.rs:1761-1780; Newton leaves) on one GPU.
+ *  group_offsets [n_groups + 1] contiguous groups over object order, 0..n;
+ *  pair_winner / pair_loser [n_pairs] global object ids of PairLogit's pairs
+ *                (weight 1, both in one group), ignored for QueryRMSE.
+ * The session is grown with cbgpu_multi_grow_tree at approx_dim 1 (target =
+ * the relevance per object); its leaf_values are the raw Newton deltas, and
+ * the resident approximant advances by the PairLogit-centred deltas x lr, as
+ * normalize_leaf_values does (boosting.rs:2844-2880).  Declines bootstrap,
+ * random_strength and more than one GPU. */
+CBGPU_API int cbgpu_rank_begin_raw(const cbgpu_begin_args* args, const int64_t* group_offsets, int32_t n_groups,
+                                   const int64_t* pair_winner, const int64_t* pair_loser, int64_t n_pairs,
+                                   const float* const* float_columns, const double* borders_flat,
+                                   const int32_t* border_counts, cbgpu_multi_session** out);
 
 /* The resident approximant, DIM-major [K * n] (flushes the pending update).
  * No counterpart in the reference. */

@@ -1,0 +1,117 @@
+"""The grouped-loss (QueryRMSE, PairLogit) device mode against upstream and the oracle.
+
+The device mode (csrc/multi.cu, cbgpu_rank_begin_raw) reproduces cb-train's
+grouped CPU branch: grouped ders (crates/cb-compute/src/ranking_der.rs),
+PairLogit's pairwise histogram weights (boosting.rs:1761-1780), Newton leaves
+and the PairLogit leaf centring (boosting.rs:2844-2880).  Trees must equal the
+oracle's; leaf values and staged approximants within the reference's 1e-5 bar.
+"""
+import json
+import os
+
+import numpy as np
+import pytest
+
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-5
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "ranking_corpus.npz")
+
+
+@pytest.fixture(scope="module")
+def cb():
+    torch = pytest.importorskip("torch")
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    import catboost_rs_b200 as cb
+    cb.load_library()
+    return cb
+
+
+@pytest.mark.parametrize("loss", ["QueryRMSE", "PairLogit"])
+def test_ranking_fixture(cb, loss):
+    z = np.load(GOLDEN)
+    p = json.loads(str(z[f"{loss}__params"]))
+    X = z["X"]
+    borders = [oracle.select_borders(X[:, f], 254, "GreedyLogSum", "Min") for f in range(X.shape[1])]
+    fp = cb.FitParams(loss=loss, depth=p["depth"], iterations=p["iterations"], learning_rate=p["learning_rate"],
+                      l2_leaf_reg=p["l2_leaf_reg"], random_seed=p["random_seed"], boost_from_average=False)
+    m = cb.fit_ranking([X[:, f].copy() for f in range(X.shape[1])], borders, z["y"], z["group_offsets"], fp,
+                       pairs=z["pairs"], staged=True)
+    np.testing.assert_array_equal(m.split_feature, z[f"{loss}__split_feature"])
+    np.testing.assert_array_equal(m.split_borders().astype(np.float32), z[f"{loss}__split_border"].astype(np.float32))
+    assert np.max(np.abs(m.leaf_values - z[f"{loss}__leaf_values"])) <= TOL
+    assert np.max(np.abs(m.staged - z[f"{loss}__staged"])) <= TOL
+
+
+def _ranking_data(n_groups, F, seed):
+    rs = np.random.RandomState(seed)
+    sizes = rs.randint(20, 121, n_groups)
+    offsets = np.concatenate([[0], np.cumsum(sizes)]).astype(np.int64)
+    n = int(offsets[-1])
+    X = rs.standard_normal((n, F)).astype(np.float32)
+    X[rs.uniform(size=X.shape) < 0.02] = np.nan
+    score = np.nan_to_num(X[:, :3]) @ np.array([1.0, -0.5, 0.25]) + 0.5 * rs.standard_normal(n)
+    y = np.zeros(n)
+    pairs = []
+    for g in range(n_groups):
+        b, e = offsets[g], offsets[g + 1]
+        q = np.quantile(score[b:e], [0.25, 0.5, 0.75])
+        y[b:e] = np.digitize(score[b:e], q)
+        for _ in range(2 * (e - b)):  # random within-group pairs, winner = higher relevance
+            i, j = rs.randint(b, e, 2)
+            if y[i] > y[j]:
+                pairs.append((i, j))
+            elif y[j] > y[i]:
+                pairs.append((j, i))
+    return X, y, offsets, np.array(pairs, dtype=np.int64)
+
+
+@pytest.mark.parametrize("loss,depth,score", [("QueryRMSE", 6, "Cosine"), ("PairLogit", 5, "Cosine"),
+                                              ("PairLogit", 4, "L2")])
+def test_ranking_matches_oracle(cb, loss, depth, score):
+    X, y, offsets, pairs = _ranking_data(300, 10, 7 + depth)
+    F = X.shape[1]
+    borders = [oracle.select_borders(X[:, f], 64) for f in range(F)]
+    fp = cb.FitParams(loss=loss, depth=depth, iterations=5, learning_rate=0.3, l2_leaf_reg=3.0,
+                      score_function=score, boost_from_average=False)
+    m = cb.fit_ranking([X[:, f].copy() for f in range(F)], borders, y, offsets, fp, pairs=pairs, staged=True)
+    bins = oracle.quantize(X.T.copy(), borders)
+    o = oracle.train_ranking(bins, [len(b) for b in borders], y, offsets, loss=loss, pairs=pairs, depth=depth,
+                             iterations=5, learning_rate=0.3, l2_leaf_reg=3.0, score_function=score)
+    np.testing.assert_array_equal(m.split_feature, o.split_feature)
+    np.testing.assert_array_equal(m.split_bin, o.split_bin)
+    assert np.max(np.abs(m.raw_leaf_values - o.raw_leaf_values)) <= TOL
+    assert np.max(np.abs(m.leaf_values - o.leaf_values)) <= TOL
+    assert np.max(np.abs(m.staged - o.staged)) <= TOL
+
+
+def test_ranking_declines_and_errors(cb):
+    from catboost_rs_b200 import CbGpuError
+    X, y, offsets, pairs = _ranking_data(20, 4, 3)
+    n, F = X.shape
+    borders = [oracle.select_borders(X[:, f], 16) for f in range(F)]
+    cols = [X[:, f].copy() for f in range(F)]
+    nb = max(len(b) for b in borders) + 1
+
+    def begin(loss="PairLogit", boot="No", offs=offsets, prs=pairs):
+        rt = cb.B200MultiRuntime()
+        cfg = cb.DeviceTrainConfig(bootstrap_type=boot)
+        ok = rt.begin_ranking_raw(loss, 3, True, 1, "Cosine", cols, borders, None, n, F, nb, 0.3, 3.0, cfg, offs, prs)
+        return rt, ok
+
+    rt, ok = begin(boot="Bayesian")
+    assert not ok and rt.decline_reason
+    rt, ok = begin(loss="RMSE")
+    assert not ok
+    with pytest.raises(CbGpuError, match="crosses group"):
+        begin(prs=np.array([[0, int(offsets[1])]]))  # winner and loser in different groups
+    with pytest.raises(CbGpuError, match="group offsets"):
+        begin(offs=np.array([0, n - 1]))
+    rt, ok = begin()
+    assert ok
+    t = rt.grow_tree_on_device(None, y, [], leaf_of_bytes=4)
+    assert len(t.splits) == 3 and t.leaf_values.size == 8 and t.leaf_of.size == n
+    rt.end_device_training()
