@@ -177,12 +177,17 @@ typedef struct {
 
 int orc_train_multiclass(const orc_multi_args* a, orc_multi_out* o);
 
+/* cholesky_solve (crates/cb-compute/src/leaf.rs:360-420): A (k x k,
+ * row-major, symmetric) x = b with scratch L (k x k) and y (k); returns 0 on
+ * a non-positive pivot. */
+int orc_cholesky_solve(const double* A, const double* b, int32_t k, double* L, double* y, double* x);
+
 /* solve_symmetric_newton (crates/cb-compute/src/leaf.rs:281-340). */
 void orc_solve_symmetric_newton(const double* sum_der, const double* sum_der2_packed, int32_t k,
                                 double scaled_l2, double* out);
 
 /* ---- grouped (ranking) losses, pointwise histograms -------------------- */
-enum { ORC_RANK_QUERYRMSE = 0, ORC_RANK_PAIRLOGIT = 1 };
+enum { ORC_RANK_QUERYRMSE = 0, ORC_RANK_PAIRLOGIT = 1, ORC_RANK_PAIRLOGIT_PAIRWISE = 2 };
 
 /* The greedy oblivious search of the scalar loop, exported for the grouped
  * loop: returns the splits taken; leaf_of gets the final leaf ids. */

@@ -55,7 +55,7 @@ static void softmax_ders(const double* a, int32_t K, int32_t y, double* p, doubl
 }
 
 /* cholesky_solve (leaf.rs:360-420); returns 0 on a non-positive pivot. */
-static int cholesky_solve(const double* A, const double* b, int32_t k, double* L, double* y, double* x) {
+int orc_cholesky_solve(const double* A, const double* b, int32_t k, double* L, double* y, double* x) {
     for (int32_t i = 0; i < k * k; ++i) L[i] = 0.0;
     for (int32_t i = 0; i < k; ++i) {
         for (int32_t j = 0; j <= i; ++j) {
@@ -114,7 +114,7 @@ void orc_solve_symmetric_newton(const double* sum_der, const double* sum_der2_pa
     for (int32_t d = 0; d < k; ++d) H[d * k + d] -= adjusted;
     for (int32_t i = 0; i < k * k; ++i) H[i] = -H[i];
     for (int32_t d = 0; d < k; ++d) nd[d] = -sum_der[d];
-    if (cholesky_solve(H, nd, k, L, y, x)) {
+    if (orc_cholesky_solve(H, nd, k, L, y, x)) {
         for (int32_t d = 0; d < k; ++d) out[d] = -x[d];
     } else {
         for (int32_t d = 0; d < k; ++d) out[d] = 0.0;

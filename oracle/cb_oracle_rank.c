@@ -1,8 +1,10 @@
 /*
  * cb_oracle_rank.c -- CPU restatement of catboost_rs's grouped (ranking)
- * losses on the pointwise-histogram oblivious loop: QueryRMSE and PairLogit
- * (crates/cb-compute/src/ranking_der.rs, crates/cb-train/src/boosting.rs
- * grouped branch, crates/cb-train/src/query_info.rs).
+ * losses on the oblivious loop: QueryRMSE and PairLogit on pointwise
+ * histograms, and PairLogitPairwise with the pairwise split scoring and
+ * Cholesky leaves (crates/cb-compute/src/ranking_der.rs, pairwise_scoring.rs,
+ * crates/cb-train/src/boosting.rs grouped branch, pairwise_leaves.rs,
+ * tree.rs:3740-3960, query_info.rs).
  *
  * TEST INFRASTRUCTURE ONLY: the parity checker for the device ranking arm.
  * The product path never calls it.  Build with -ffp-contract=off.
@@ -22,6 +24,11 @@
  *     object-weight sum;
  *  5. normalize_leaf_values (boosting.rs:2844-2880): PairLogit subtracts the
  *     document-weighted mean leaf value, then x lr (f32-narrowed).
+ * PairLogitPairwise replaces 3-4: per level and feature the der sums
+ * [leaf][bucket] and pair statistics [leaf][leaf][bucket], a running
+ * 2P x 2P weight system per border with a Cholesky leaf solve and score
+ * (pairwise_scoring.rs:101-580); leaves from the leaf pair-weight system with
+ * the raw l2 (pairwise_leaves.rs:51-242); the same centring and x lr.
  */
 #include "cb_oracle.h"
 
@@ -62,6 +69,191 @@ static int build_competitors(const orc_rank_args* a, competitors* c) {
     return 0;
 }
 
+/* ---- pairwise scoring (crates/cb-compute/src/pairwise_scoring.rs) ------- */
+
+/* make_zero_average (pairwise_leaves.rs:202-212) */
+static void make_zero_average(double* v, int32_t n) {
+    if (n == 0) return;
+    const double avg = orc_sum_f64(v, n) / (double)n;
+    for (int32_t i = 0; i < n; ++i) v[i] -= avg;
+}
+
+/* calculate_pairwise_leaf_values (pairwise_leaves.rs:113-200): the n x n
+ * weight matrix w (row-major) and der vector -> n zero-averaged values. */
+static void pairwise_leaf_values(const double* w, const double* der, int32_t n, double l2, double prior,
+                                 double* out) {
+    if (n == 0) return;
+    if (n == 1) {
+        out[0] = 0.0;
+        return;
+    }
+    const double cell_prior = 1.0 / (double)n;
+    const double non_diag = -prior * cell_prior;
+    const double diag = prior * (1.0 - cell_prior) + l2;
+    if (n == 2) {
+        const double den = w[0] + diag;
+        out[0] = den != 0.0 ? der[0] / den : 0.0;
+        out[1] = 0.0;
+        make_zero_average(out, 2);
+        return;
+    }
+    const int32_t m = n - 1;
+    double* A = (double*)calloc((size_t)m * m * 2 + (size_t)m * 2, sizeof(double));
+    double* L = A + (size_t)m * m;
+    double* y = L + (size_t)m * m;
+    double* x = y + m;
+    for (int32_t r = 0; r < m; ++r) {
+        for (int32_t c = 0; c < r; ++c) {
+            const double v = w[(size_t)r * n + c] + non_diag;
+            A[(size_t)r * m + c] = v;
+            A[(size_t)c * m + r] = v;
+        }
+        A[(size_t)r * m + r] = w[(size_t)r * n + r] + diag;
+    }
+    if (orc_cholesky_solve(A, der, m, L, y, x)) {
+        for (int32_t i = 0; i < m; ++i) out[i] = x[i];
+    } else {
+        for (int32_t i = 0; i < m; ++i) out[i] = 0.0;
+    }
+    out[m] = 0.0;
+    make_zero_average(out, n);
+    free(A);
+}
+
+/* calculate_score (pairwise_scoring.rs:367-391) */
+static double pairwise_score(const double* avrg, const double* der, const double* w, int32_t n, double* tmp) {
+    double outer = 0.0;
+    for (int32_t x = 0; x < n; ++x) {
+        for (int32_t y = 0; y < n; ++y) tmp[y] = avrg[y] * w[(size_t)x * n + y];
+        const double sub = orc_sum_f64(tmp, n);
+        outer += avrg[x] * (der[x] - 0.5 * sub);
+    }
+    return outer;
+}
+
+#define WS(r, c) ws[(size_t)(r) * n2 + (c)]
+
+/* One feature's pairwise scores over its B - 1 borders at a level with P
+ * leaves (compute_der_sums + compute_pair_weight_statistics +
+ * calculate_pairwise_score, pairwise_scoring.rs:101-580): the bucket of a
+ * row is its bin. */
+static void pairwise_feature_scores(const uint8_t* col, int64_t n, int32_t B, const int32_t* leaf_of, int32_t P,
+                                    const double* der1, const int64_t* pw, const int64_t* pl, int64_t n_pairs,
+                                    double l2, double prior, double* scores) {
+    const int32_t n2 = 2 * P;
+    double* ds = (double*)calloc((size_t)P * B, sizeof(double));        /* [P][B] */
+    double* sm = (double*)calloc((size_t)P * P * B, sizeof(double));    /* smaller [P][P][B] */
+    double* gr = (double*)calloc((size_t)P * P * B, sizeof(double));    /* greater-right [P][P][B] */
+    double* ws = (double*)calloc((size_t)n2 * n2, sizeof(double));
+    double* dsum = (double*)calloc((size_t)n2, sizeof(double));
+    double* lv = (double*)malloc(sizeof(double) * (size_t)n2);
+    double* tmp = (double*)malloc(sizeof(double) * (size_t)(n2 > 2 * B ? n2 : 2 * B));
+    for (int64_t i = 0; i < n; ++i) ds[(size_t)leaf_of[i] * B + col[i]] += der1[i];
+    for (int64_t k = 0; k < n_pairs; ++k) {
+        const int64_t wv = pw[k], lo = pl[k];
+        if (wv == lo) continue;
+        const int32_t wb = col[wv], wl = leaf_of[wv], lb = col[lo], ll = leaf_of[lo];
+        if (wb > lb) {
+            sm[((size_t)ll * P + wl) * B + lb] -= 1.0;
+            gr[((size_t)ll * P + wl) * B + wb] -= 1.0;
+        } else {
+            sm[((size_t)wl * P + ll) * B + wb] -= 1.0;
+            gr[((size_t)wl * P + ll) * B + lb] -= 1.0;
+        }
+    }
+    for (int32_t q = 0; q < P; ++q) dsum[2 * q + 1] += orc_sum_f64(ds + (size_t)q * B, B);
+    for (int32_t y = 0; y < P; ++y)
+        for (int32_t x = y + 1; x < P; ++x) {
+            for (int32_t b = 0; b < B; ++b) {
+                tmp[2 * b] = sm[((size_t)x * P + y) * B + b];
+                tmp[2 * b + 1] = sm[((size_t)y * P + x) * B + b];
+            }
+            const double t = orc_sum_f64(tmp, 2 * B);
+            WS(2 * y + 1, 2 * x + 1) += t;
+            WS(2 * x + 1, 2 * y + 1) += t;
+            WS(2 * x + 1, 2 * x + 1) += -t;
+            WS(2 * y + 1, 2 * y + 1) += -t;
+        }
+    for (int32_t b = 0; b < B - 1; ++b) {
+        for (int32_t y = 0; y < P; ++y) {
+            const double dd = ds[(size_t)y * B + b];
+            dsum[2 * y] += dd;
+            dsum[2 * y + 1] += -dd;
+            const double wd = sm[((size_t)y * P + y) * B + b] - gr[((size_t)y * P + y) * B + b];
+            WS(2 * y, 2 * y + 1) += wd;
+            WS(2 * y + 1, 2 * y) += wd;
+            WS(2 * y, 2 * y) += -wd;
+            WS(2 * y + 1, 2 * y + 1) += -wd;
+            for (int32_t x = y + 1; x < P; ++x) {
+                const size_t ixy = ((size_t)x * P + y) * B + b, iyx = ((size_t)y * P + x) * B + b;
+                const double w00 = gr[ixy] + gr[iyx];
+                const double w01 = sm[ixy] - gr[ixy];
+                const double w10 = sm[iyx] - gr[iyx];
+                const double w11 = -(sm[ixy] + sm[iyx]);
+                WS(2 * x, 2 * y) += w00;
+                WS(2 * y, 2 * x) += w00;
+                WS(2 * x, 2 * y + 1) += w01;
+                WS(2 * y + 1, 2 * x) += w01;
+                WS(2 * x + 1, 2 * y) += w10;
+                WS(2 * y, 2 * x + 1) += w10;
+                WS(2 * x + 1, 2 * y + 1) += w11;
+                WS(2 * y + 1, 2 * x + 1) += w11;
+                WS(2 * y, 2 * y) += -(w00 + w10);
+                WS(2 * x, 2 * x) += -(w00 + w01);
+                WS(2 * x + 1, 2 * x + 1) += -(w10 + w11);
+                WS(2 * y + 1, 2 * y + 1) += -(w01 + w11);
+            }
+        }
+        pairwise_leaf_values(ws, dsum, n2, l2, prior, lv);
+        scores[b] = pairwise_score(lv, dsum, ws, n2, tmp);
+    }
+    free(ds);
+    free(sm);
+    free(gr);
+    free(ws);
+    free(dsum);
+    free(lv);
+    free(tmp);
+}
+#undef WS
+
+/* the pairwise greedy search (tree.rs:3861-3960): per level, every feature's
+ * pairwise scores, strict first-wins over (feature, border). */
+static int pairwise_search(const orc_rank_args* a, const double* der1, const int64_t* pw, const int64_t* pl,
+                           int64_t n_pairs, int32_t* feat, int32_t* sbin, int32_t* leaf_of) {
+    const int64_t n = a->n;
+    double* sc = (double*)malloc(sizeof(double) * 256);
+    for (int64_t i = 0; i < n; ++i) leaf_of[i] = 0;
+    for (int32_t level = 0; level < a->depth; ++level) {
+        const int32_t P = 1 << level;
+        double best = -INFINITY;
+        int32_t bf = -1, bb = -1;
+        for (int32_t f = 0; f < a->n_features; ++f) {
+            const int32_t nb = a->border_counts[f];
+            if (nb == 0) continue;
+            pairwise_feature_scores(a->bins_fm + (size_t)f * n, n, nb + 1, leaf_of, P, der1, pw, pl, n_pairs,
+                                    a->l2_leaf_reg, 0.1, sc);
+            for (int32_t b = 0; b < nb; ++b)
+                if (sc[b] > best) {
+                    best = sc[b];
+                    bf = f;
+                    bb = b;
+                }
+        }
+        if (bf < 0) {
+            free(sc);
+            return -1;
+        }
+        feat[level] = bf;
+        sbin[level] = bb;
+        const uint8_t* col = a->bins_fm + (size_t)bf * n;
+        for (int64_t i = 0; i < n; ++i)
+            if ((int32_t)col[i] > bb) leaf_of[i] += P;
+    }
+    free(sc);
+    return a->depth;
+}
+
 int orc_train_ranking(const orc_rank_args* a, orc_rank_out* o) {
     const int64_t n = a->n;
     const int32_t F = a->n_features, D = a->depth, L = 1 << D;
@@ -71,7 +263,8 @@ int orc_train_ranking(const orc_rank_args* a, orc_rank_out* o) {
     for (int32_t f = 0; f < F; ++f)
         if (a->border_counts[f] + 1 > NB) NB = a->border_counts[f] + 1;
     competitors cp = {NULL, NULL};
-    if (a->loss == ORC_RANK_PAIRLOGIT && build_competitors(a, &cp) != 0) {
+    const int pairlogit = a->loss == ORC_RANK_PAIRLOGIT || a->loss == ORC_RANK_PAIRLOGIT_PAIRWISE;
+    if (pairlogit && build_competitors(a, &cp) != 0) {
         free(cp.start);
         free(cp.loser);
         return -2;
@@ -93,7 +286,7 @@ int orc_train_ranking(const orc_rank_args* a, orc_rank_out* o) {
     double* lw = (double*)malloc(sizeof(double) * L);
 
     /* histogram weights: pairwise weights for PairLogit, object weights otherwise */
-    if (a->loss == ORC_RANK_PAIRLOGIT) {
+    if (pairlogit) {
         for (int64_t i = 0; i < n; ++i) eff[i] = 0.0;
         for (int32_t g = 0; g < a->n_groups; ++g)
             for (int64_t wi = a->group_offsets[g]; wi < a->group_offsets[g + 1]; ++wi)
@@ -105,6 +298,19 @@ int orc_train_ranking(const orc_rank_args* a, orc_rank_out* o) {
         for (int64_t i = 0; i < n; ++i) eff[i] = w[i];
     }
     for (int64_t i = 0; i < n; ++i) sh[i] = eff[i]; /* no bootstrap: control 1, sample weight 1 */
+
+    /* flatten_global_pairs (tree.rs:3747-3760): group, winner, competitor order */
+    int64_t n_flat = 0;
+    int64_t* pairs_w = (int64_t*)malloc(sizeof(int64_t) * (size_t)(a->n_pairs > 0 ? a->n_pairs : 1));
+    int64_t* pairs_l = (int64_t*)malloc(sizeof(int64_t) * (size_t)(a->n_pairs > 0 ? a->n_pairs : 1));
+    if (pairlogit)
+        for (int32_t g = 0; g < a->n_groups; ++g)
+            for (int64_t wi = a->group_offsets[g]; wi < a->group_offsets[g + 1]; ++wi)
+                for (int64_t k = cp.start[wi]; k < cp.start[wi + 1]; ++k) {
+                    pairs_w[n_flat] = wi;
+                    pairs_l[n_flat] = cp.loser[k];
+                    ++n_flat;
+                }
 
     orc_rng rng;
     orc_rng_from_seed(&rng, a->random_seed);
@@ -151,12 +357,22 @@ int orc_train_ranking(const orc_rank_args* a, orc_rank_out* o) {
             tf[l] = -1;
             tb[l] = -1;
         }
-        int32_t err = 0;
-        int taken = orc_search_tree(n, F, NB, D, a->score_function, a->bins_fm, a->border_counts, d1, sh, scaled_l2,
+        int taken;
+        if (a->loss == ORC_RANK_PAIRLOGIT_PAIRWISE) {
+            /* pairwise scoring over the flattened competitor pairs (tree.rs:3747-3760) */
+            taken = pairwise_search(a, d1, pairs_w, pairs_l, n_flat, tf, tb, leaf);
+            if (taken < 0) {
+                rc = -3;
+                break;
+            }
+        } else {
+            int32_t err = 0;
+            taken = orc_search_tree(n, F, NB, D, a->score_function, a->bins_fm, a->border_counts, d1, sh, scaled_l2,
                                     0, &rng, tf, tb, leaf, &err);
-        if (err) {
-            rc = -3;
-            break;
+            if (err) {
+                rc = -3;
+                break;
+            }
         }
         const int32_t nl = 1 << taken;
         /* 4. Newton leaves over unit leaf weights, ordered per-leaf sums */
@@ -176,9 +392,28 @@ int orc_train_ranking(const orc_rank_args* a, orc_rank_out* o) {
             lw[q] = sd[3 * q + 2];
         }
         free(sd);
+        if (a->loss == ORC_RANK_PAIRLOGIT_PAIRWISE) {
+            /* compute_pairwise_leaf_deltas (pairwise_leaves.rs:219-242): the
+             * leaf pair-weight matrix in group / winner / competitor order, the
+             * ordered leaf der sums, the Cholesky system with the raw l2 */
+            double* wsum = (double*)calloc((size_t)nl * nl, sizeof(double));
+            double* dsl = (double*)calloc((size_t)nl, sizeof(double));
+            for (int64_t k = 0; k < n_flat; ++k) {
+                const int32_t wl = leaf[pairs_w[k]], ll = leaf[pairs_l[k]];
+                if (wl == ll) continue;
+                wsum[(size_t)wl * nl + ll] -= 1.0;
+                wsum[(size_t)ll * nl + wl] -= 1.0;
+                wsum[(size_t)wl * nl + wl] += 1.0;
+                wsum[(size_t)ll * nl + ll] += 1.0;
+            }
+            for (int64_t i = 0; i < n; ++i) dsl[leaf[i]] += d1[i];
+            pairwise_leaf_values(wsum, dsl, nl, a->l2_leaf_reg, 0.1, lv);
+            free(wsum);
+            free(dsl);
+        }
         if (o->raw_leaf_values) memcpy(o->raw_leaf_values + (size_t)it * L, lv, sizeof(double) * L);
         /* 5. normalize_leaf_values */
-        if (a->loss == ORC_RANK_PAIRLOGIT) {
+        if (pairlogit) {
             const double total = orc_sum_f64(lw, nl);
             if (fabs(total) > 1e-9) {
                 for (int32_t q = 0; q < nl; ++q) tmp[q] = lv[q] * lw[q];
@@ -193,6 +428,8 @@ int orc_train_ranking(const orc_rank_args* a, orc_rank_out* o) {
     }
     free(cp.start);
     free(cp.loser);
+    free(pairs_w);
+    free(pairs_l);
     free(w); free(approx); free(d1); free(d2); free(eff); free(sh); free(tmp); free(leaf); free(lv); free(lw);
     return rc;
 }

@@ -89,7 +89,7 @@ class _RankOut(C.Structure):
                 ("raw_leaf_values", C.c_void_p), ("staged", C.c_void_p)]
 
 
-RANK_LOSS = {"QueryRMSE": 0, "PairLogit": 1}
+RANK_LOSS = {"QueryRMSE": 0, "PairLogit": 1, "PairLogitPairwise": 2}
 
 
 def lib():
@@ -401,7 +401,8 @@ class OracleRankFit:
 def train_ranking(bins_fm, border_counts, target, group_offsets, *, loss="QueryRMSE", pairs=None, depth=6,
                   iterations=10, learning_rate=0.1, l2_leaf_reg=3.0, score_function="Cosine", random_seed=0,
                   weights=None, staged=True) -> OracleRankFit:
-    """The reference's grouped-loss CPU loop (QueryRMSE / PairLogit, pointwise histograms, Newton leaves)."""
+    """The reference's grouped-loss CPU loop: QueryRMSE / PairLogit (pointwise histograms, Newton
+    leaves) and PairLogitPairwise (pairwise scoring, Cholesky pairwise leaves)."""
     bins = np.ascontiguousarray(bins_fm, dtype=np.uint8)
     F, n = bins.shape
     bc = np.ascontiguousarray(border_counts, dtype=np.int32)

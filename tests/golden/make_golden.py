@@ -234,7 +234,7 @@ def multiclass_fixture(ref):
 
 
 def ranking_fixtures(ref):
-    """Upstream QueryRMSE / PairLogit fixtures on the reference's frozen ranking
+    """Upstream QueryRMSE / PairLogit / PairLogitPairwise fixtures on the reference's frozen ranking
     corpus (12 objects, 5 contiguous groups, 7 explicit pairs): inputs, group
     offsets, pairs, and per loss the trees, leaf values and staged approximants."""
     fx = os.path.join(ref, "crates/cb-oracle/fixtures/ranking_corpus")
@@ -244,9 +244,12 @@ def ranking_fixtures(ref):
                   y=np.load(os.path.join(fx, "inputs/y.npy")).astype(np.float64), group_offsets=offsets,
                   pairs=np.load(os.path.join(fx, "inputs/pairs.npy")).astype(np.int64))
     losses = []
-    for loss in ("QueryRMSE", "PairLogit"):
+    for loss in ("QueryRMSE", "PairLogit", "PairLogitPairwise"):
         cfg = json.loads(_read(os.path.join(fx, loss, "config.json")))
         model = json.loads(_read(os.path.join(fx, loss, "model.json")))
+        mparams = model["model_info"].get("params")
+        mparams = json.loads(mparams) if isinstance(mparams, str) else (mparams or {})
+        l2 = float(mparams.get("tree_learner_options", {}).get("l2_leaf_reg", 3.0))
         trees = model["oblivious_trees"]
         arrays[f"{loss}__split_feature"] = np.array([[s["float_feature_index"] for s in t["splits"]] for t in trees],
                                                     dtype=np.int32)
@@ -255,7 +258,7 @@ def ranking_fixtures(ref):
         arrays[f"{loss}__staged"] = np.load(os.path.join(fx, loss, "staged.npy")).reshape(len(trees), -1)
         arrays[f"{loss}__params"] = np.array(json.dumps({
             "depth": int(cfg["depth"]), "iterations": int(cfg["iterations"]),
-            "learning_rate": float(cfg["learning_rate"]), "l2_leaf_reg": float(cfg.get("l2_leaf_reg", 3.0)),
+            "learning_rate": float(cfg["learning_rate"]), "l2_leaf_reg": l2,
             "random_seed": int(cfg["random_seed"])}))
         losses.append(loss)
     np.savez_compressed(os.path.join(OUT, "ranking_corpus.npz"), **arrays)

@@ -1,9 +1,12 @@
-"""Pin the oracle's grouped-loss loop (QueryRMSE, PairLogit) to upstream.
+"""Pin the oracle's grouped-loss loop (QueryRMSE, PairLogit, PairLogitPairwise) to upstream.
 
 tests/golden/ranking_corpus.npz comes from the reference's frozen ranking
 corpus (crates/cb-oracle/fixtures/ranking_corpus: 12 objects in 5 contiguous
-groups, 7 explicit pairs, depth 2, 5 iterations, lr 0.3, Newton leaves), which
-the reference's own ranking oracle tests train against.  Trees are compared
+groups, 7 explicit pairs, depth 2, 5 iterations, lr 0.3), which the
+reference's own ranking oracle tests train against.  PairLogitPairwise scores
+splits with the pairwise statistics and a per-candidate Cholesky solve
+(crates/cb-compute/src/pairwise_scoring.rs) and takes its leaves from the
+pairwise Cholesky system (crates/cb-train/src/pairwise_leaves.rs).  Trees are compared
 both with the full standalone GreedyLogSum border set (border_count 254) and
 with the model's own borders; leaf values and staged approximants at the
 reference's 1e-5 bar (crates/cb-oracle/src/compare.rs:46-148).
@@ -34,7 +37,7 @@ def _fit(d, loss, borders, **kw):
     return oracle.train_ranking(bins, [len(b) for b in borders], d["y"], d["group_offsets"], **args)
 
 
-@pytest.mark.parametrize("loss", ["QueryRMSE", "PairLogit"])
+@pytest.mark.parametrize("loss", ["QueryRMSE", "PairLogit", "PairLogitPairwise"])
 @pytest.mark.parametrize("border_set", ["full", "model"])
 def test_ranking_matches_upstream(loss, border_set):
     d = _load()
