@@ -86,7 +86,8 @@ def load(path: str = LIB_PATH):
         "cbgpu_multi_begin_raw": ([C.POINTER(BeginArgs), i32, vp, vp, vp, C.POINTER(vp)], C.c_int),
         "cbgpu_multi_grow_tree": ([vp, vp, vp, i64, vp, i64, vp, vp, vp, vp, vp, i32], C.c_int),
         "cbgpu_multi_approx": ([vp, vp, i64], C.c_int),
-        "cbgpu_rank_begin_raw": ([C.POINTER(BeginArgs), vp, i32, vp, vp, i64, vp, vp, vp, C.POINTER(vp)], C.c_int),
+        "cbgpu_rank_begin_raw": ([C.POINTER(BeginArgs), vp, i32, vp, vp, i64, C.c_double, vp, vp, vp, C.POINTER(vp)],
+                                 C.c_int),
         "cbgpu_multi_end": ([vp], C.c_int),
         "cbgpu_nccl_unique_id": ([vp], C.c_int),
         "cbgpu_version": ([], C.c_char_p),

@@ -232,10 +232,10 @@ def normalize_leaf_values(pairwise: bool, lr: float, leaf_weights, raw) -> np.nd
 def fit_ranking(float_columns: Sequence[np.ndarray], borders: Sequence[Sequence[float]], target, group_offsets,
                 params: FitParams, pairs=None, weights=None, *, staged: bool = False,
                 device: int = 0) -> RankingModel:
-    """QueryRMSE / PairLogit fit (params.loss) on raw f32 columns with fixed
-    borders: cb-train's grouped loop (pointwise histograms, Newton leaves)
-    over the device's ranking arm; leaf normalisation on the host as cb-train
-    does it."""
+    """QueryRMSE / PairLogit / PairLogitPairwise fit (params.loss) on raw f32
+    columns with fixed borders: cb-train's grouped loop (pointwise histograms
+    and Newton leaves, or pairwise scoring and Cholesky leaves) over the
+    device's ranking arm; leaf normalisation on the host as cb-train does it."""
     p = params
     cols = [np.ascontiguousarray(c, dtype=np.float32) for c in float_columns]
     F = len(cols)
@@ -249,7 +249,7 @@ def fit_ranking(float_columns: Sequence[np.ndarray], borders: Sequence[Sequence[
     rt = B200MultiRuntime()
     n_bins = max(len(b) for b in borders) + 1
     ok = rt.begin_ranking_raw(p.loss, p.depth, True, 1, p.score_function, cols, borders, w, n, F, n_bins, lr,
-                              scaled_l2, cfg, group_offsets, pairs)
+                              scaled_l2, cfg, group_offsets, pairs, l2_leaf_reg=p.l2_leaf_reg)
     if not ok:
         raise RuntimeError(f"device declined: {rt.decline_reason}")
     T, D = p.iterations, p.depth
@@ -267,7 +267,8 @@ def fit_ranking(float_columns: Sequence[np.ndarray], borders: Sequence[Sequence[
                 sf[it, l], sb[it, l] = f, b
             raw[it] = tree.leaf_values
             leaf_w = np.bincount(tree.leaf_of.astype(np.int64), weights=doc_w, minlength=L)
-            lv[it] = normalize_leaf_values(p.loss == "PairLogit", lr, leaf_w, tree.leaf_values)
+            lv[it] = normalize_leaf_values(p.loss in ("PairLogit", "PairLogitPairwise"), lr, leaf_w,
+                                           tree.leaf_values)
             if staged:
                 st[it] = rt.resident_approx()[0]
     finally:

@@ -486,7 +486,8 @@ __global__ void mc_apply_pending_kernel(int64_t n, int K, int L, double* __restr
 
 // ---- ranking mode (grouped losses, K = 1) ----------------------------------
 
-enum : int { kRankQueryRmse = 0, kRankPairLogit = 1 };
+enum : int { kRankQueryRmse = 0, kRankPairLogit = 1, kRankPairLogitPairwise = 2 };
+constexpr double kPairwisePrior = 0.1;  // PairwiseNonDiagReg default (oblivious_tree_options.cpp:16)
 
 // Grouped derivatives (calc_ders_for_queries, crates/cb-compute/src/
 // ranking_der.rs:139-440), one thread per group in the reference's order, so
@@ -630,6 +631,299 @@ __global__ void rk_newton_kernel(int L, int pairwise, const unsigned long long* 
     }
 }
 
+// ---- PairLogitPairwise: pairwise split scoring and Cholesky pairwise leaves
+//
+// The reference scores a candidate border b of feature f at a level with P
+// leaves by building a running 2P x 2P pair-weight system over the border
+// buckets 0..b (calculate_pairwise_score, crates/cb-compute/src/
+// pairwise_scoring.rs:367-580) and solving it with a Cholesky factor per
+// border.  With unit pair weights every entry of that system is an integer
+// pair count, so the system at border b equals one built directly from the
+// bin-prefix pair statistics: candidates are independent here, one block each.
+
+constexpr int kPwThreads = 128;
+constexpr int kPwMaxDepth = 8;                 // P <= 128 leaves at the last level
+constexpr int kPwSmemMaxN2 = 64;               // systems up to 64 x 64 stay in shared memory
+constexpr int kPwGlobalBlocks = 148 * 2;       // global-scratch slots for larger systems
+constexpr size_t kPwMaxStatBytes = (size_t)16 << 30;
+
+// doubles of scratch one candidate needs: ws (n2^2), the factor (m^2) and
+// dsum, lv, y, x, term (n2 each)
+__host__ __device__ inline size_t pw_scratch_doubles(int n2) {
+    const size_t m = (size_t)(n2 > 1 ? n2 - 1 : 1);
+    return (size_t)n2 * n2 + m * m + 5 * (size_t)n2;
+}
+
+// Pair statistics of one level (compute_pair_weight_statistics,
+// pairwise_scoring.rs:163-198), buckets = bins, pair weight 1:
+//   wb > lb: smaller[ll][wl][lb] -= 1, greater[ll][wl][wb] -= 1
+//   else:    smaller[wl][ll][wb] -= 1, greater[wl][ll][lb] -= 1
+// int32 counts (exact in any order): st[f][a][c][bin][2] = (smaller, greater).
+__global__ void rk_pairstat_kernel(int64_t n_pairs, int64_t n, int P, int NB, const int64_t* __restrict__ pw,
+                                   const int64_t* __restrict__ pl, const uint8_t* __restrict__ bins_fm,
+                                   const uint16_t* __restrict__ leaf, int32_t* __restrict__ stats) {
+    const int f = blockIdx.y;
+    const uint8_t* col = bins_fm + (size_t)f * (size_t)n;
+    int32_t* st = stats + (size_t)f * P * P * NB * 2;
+    for (int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < n_pairs; k += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t w = pw[k], l = pl[k];
+        if (w == l) continue;
+        const int wb = col[w], lb = col[l], wl = leaf[w], ll = leaf[l];
+        if (wl >= P || ll >= P || wb >= NB || lb >= NB) continue;
+        if (wb > lb) {
+            atomicSub(&st[(((size_t)ll * P + wl) * NB + lb) * 2 + 0], 1);
+            atomicSub(&st[(((size_t)ll * P + wl) * NB + wb) * 2 + 1], 1);
+        } else {
+            atomicSub(&st[(((size_t)wl * P + ll) * NB + wb) * 2 + 0], 1);
+            atomicSub(&st[(((size_t)wl * P + ll) * NB + lb) * 2 + 1], 1);
+        }
+    }
+}
+
+// Inclusive prefix over bins of every (feature, leaf, leaf, kind) row.
+__global__ void rk_pairprefix_kernel(int64_t rows, int NB, int32_t* __restrict__ st) {
+    for (int64_t r = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; r < rows; r += (int64_t)gridDim.x * blockDim.x) {
+        int32_t* row = st + (size_t)(r >> 1) * NB * 2 + (r & 1);
+        int32_t run = 0;
+        for (int b = 0; b < NB; ++b) {
+            run += row[(size_t)b * 2];
+            row[(size_t)b * 2] = run;
+        }
+    }
+}
+
+// make_zero_average (crates/cb-train/src/pairwise_leaves.rs:202-212), one thread.
+__device__ void pw_zero_average(double* v, int n) {
+    double s = 0.0;
+    for (int i = 0; i < n; ++i) s = __dadd_rn(s, v[i]);
+    const double avg = __ddiv_rn(s, (double)n);
+    for (int i = 0; i < n; ++i) v[i] = __dsub_rn(v[i], avg);
+}
+
+// cholesky_solve (crates/cb-compute/src/leaf.rs:360-420) by the whole block:
+// A (m x m, lower triangle) is factored in place, right-looking, but every
+// entry subtracts its products in ascending column order and is divided by
+// the same pivot, so each value rounds as in the reference's left-looking
+// loops; the substitutions run on thread 0 in the reference's order.  The
+// result is block-uniform: false on a non-positive pivot.
+__device__ bool pw_cholesky_block(double* A, const double* rhs, int m, double* y, double* x, int* s_flag) {
+    const int tid = threadIdx.x, nt = blockDim.x;
+    if (tid == 0) *s_flag = 0;
+    __syncthreads();
+    for (int j = 0; j < m; ++j) {
+        if (tid == 0) {
+            const double d = A[(size_t)j * m + j];
+            if (d <= 0.0) *s_flag = 1;
+            else A[(size_t)j * m + j] = sqrt(d);
+        }
+        __syncthreads();
+        if (*s_flag) return false;
+        const double piv = A[(size_t)j * m + j];
+        for (int i = j + 1 + tid; i < m; i += nt) A[(size_t)i * m + j] = __ddiv_rn(A[(size_t)i * m + j], piv);
+        __syncthreads();
+        const int rem = m - j - 1;
+        for (int idx = tid; idx < rem * rem; idx += nt) {
+            const int ii = idx / rem, kk = idx - ii * rem;
+            if (kk > ii) continue;
+            const int i = j + 1 + ii, k = j + 1 + kk;
+            A[(size_t)i * m + k] = __dsub_rn(A[(size_t)i * m + k], __dmul_rn(A[(size_t)i * m + j], A[(size_t)k * m + j]));
+        }
+        __syncthreads();
+    }
+    if (tid == 0) {
+        for (int i = 0; i < m; ++i) {
+            double sum = rhs[i];
+            for (int p = 0; p < i; ++p) sum = __dsub_rn(sum, __dmul_rn(A[(size_t)i * m + p], y[p]));
+            y[i] = __ddiv_rn(sum, A[(size_t)i * m + i]);
+        }
+        for (int i = m - 1; i >= 0; --i) {
+            double sum = y[i];
+            for (int p = i + 1; p < m; ++p) sum = __dsub_rn(sum, __dmul_rn(A[(size_t)p * m + i], x[p]));
+            x[i] = __ddiv_rn(sum, A[(size_t)i * m + i]);
+        }
+    }
+    __syncthreads();
+    return true;
+}
+
+// calculate_pairwise_leaf_values (pairwise_leaves.rs:113-200) by the whole
+// block: w is n x n, out gets n zero-averaged values; A holds (n-1)^2, y and
+// x (n-1) each.
+__device__ void pw_leaf_values_block(const double* w, const double* der, int n, double l2, double* out, double* A,
+                                     double* y, double* x, int* s_flag) {
+    const int tid = threadIdx.x;
+    if (n <= 2) {
+        if (tid == 0) {
+            if (n == 1) {
+                out[0] = 0.0;
+            } else {
+                const double cp = __ddiv_rn(1.0, 2.0);
+                const double dg = __dadd_rn(__dmul_rn(kPairwisePrior, __dsub_rn(1.0, cp)), l2);
+                const double den = __dadd_rn(w[0], dg);
+                out[0] = den != 0.0 ? __ddiv_rn(der[0], den) : 0.0;
+                out[1] = 0.0;
+                pw_zero_average(out, 2);
+            }
+        }
+        __syncthreads();
+        return;
+    }
+    const double cp = __ddiv_rn(1.0, (double)n);
+    const double nd = __dmul_rn(-kPairwisePrior, cp);
+    const double dg = __dadd_rn(__dmul_rn(kPairwisePrior, __dsub_rn(1.0, cp)), l2);
+    const int m = n - 1;
+    // the system's lower triangle mirrored (the reference reads w[r][c], c < r)
+    for (int idx = tid; idx < m * m; idx += blockDim.x) {
+        const int r = idx / m, c = idx - r * m;
+        const int hi = r > c ? r : c, lo = r > c ? c : r;
+        A[idx] = r == c ? __dadd_rn(w[(size_t)r * n + r], dg) : __dadd_rn(w[(size_t)hi * n + lo], nd);
+    }
+    __syncthreads();
+    const bool ok = pw_cholesky_block(A, der, m, y, x, s_flag);
+    if (tid == 0) {
+        for (int i = 0; i < m; ++i) out[i] = ok ? x[i] : 0.0;
+        out[m] = 0.0;
+        pw_zero_average(out, n);
+    }
+    __syncthreads();
+}
+
+// One off-diagonal entry (r != c) of the pair-weight system of border b
+// (the running sums of pairwise_scoring.rs:420-540 evaluated in closed
+// form); leaf a of row r = r / 2, its side r % 2 (1: bins above b).
+__device__ __forceinline__ double pw_offdiag(int r, int c, int P, int NB, int b, const int32_t* __restrict__ st) {
+    auto S = [&](int u, int v, int bin) -> long long { return st[(((size_t)u * P + v) * NB + bin) * 2 + 0]; };
+    auto G = [&](int u, int v, int bin) -> long long { return st[(((size_t)u * P + v) * NB + bin) * 2 + 1]; };
+    const int a = r >> 1, sa = r & 1, d = c >> 1, sd = c & 1;
+    if (a == d) return (double)(S(a, a, b) - G(a, a, b));  // the two sides of one leaf
+    const int y = a < d ? a : d, x = a < d ? d : a;
+    const int sy = a < d ? sa : sd, sx = a < d ? sd : sa;
+    if (sy == 1 && sx == 1)  // every pair between the leaves minus those at or below b
+        return (double)((S(x, y, NB - 1) + S(y, x, NB - 1)) - (S(x, y, b) + S(y, x, b)));
+    if (sy == 0 && sx == 0) return (double)(G(x, y, b) + G(y, x, b));
+    if (sx == 0) return (double)(S(x, y, b) - G(x, y, b));  // x below, y above
+    return (double)(S(y, x, b) - G(y, x, b));               // x above, y below
+}
+
+// Scores of every candidate (feature, border) at a level with P leaves
+// (calculate_pairwise_score + calculate_score, pairwise_scoring.rs:367-580):
+// block per candidate, the der sums from the level histogram's bin prefix of
+// channel 0 (exact int64), the pair counts from the prefixed statistics.
+// Scratch: dynamic shared memory when 2P <= 64, else a global slot per block.
+__global__ void __launch_bounds__(kPwThreads)
+rk_pairscore_kernel(int P, int F, int NB, int C, const unsigned long long* __restrict__ pre,
+                    const int32_t* __restrict__ stats, const int32_t* __restrict__ border_counts,
+                    const McState* __restrict__ ms, double l2, int use_smem, double* __restrict__ gscratch,
+                    double* __restrict__ scores) {
+    extern __shared__ double pw_smem[];
+    __shared__ int s_flag;
+    const int n2 = 2 * P, m = n2 - 1, tid = threadIdx.x;
+    double* ws = use_smem ? pw_smem : gscratch + (size_t)blockIdx.x * pw_scratch_doubles(n2);
+    double* A = ws + (size_t)n2 * n2;
+    double* dsum = A + (size_t)(m > 0 ? m : 1) * (m > 0 ? m : 1);
+    double* lv = dsum + n2;
+    double* y = lv + n2;
+    double* x = y + n2;
+    double* term = x + n2;
+    const double inv = ldexp(1.0, -ms->hist_shift);
+    const int64_t cand = (int64_t)F * NB;
+    for (int64_t k = blockIdx.x; k < cand; k += gridDim.x) {
+        const int f = (int)(k / NB), b = (int)(k - (int64_t)f * NB);
+        if (b >= border_counts[f] || b >= NB - 1) {  // block-uniform
+            if (tid == 0) scores[k] = -INFINITY;
+            continue;
+        }
+        const int32_t* st = stats + (size_t)f * P * P * NB * 2;
+        for (int idx = tid; idx < n2 * n2; idx += blockDim.x) {
+            const int r = idx / n2, c = idx - r * n2;
+            ws[idx] = r == c ? 0.0 : pw_offdiag(r, c, P, NB, b, st);
+        }
+        for (int q = tid; q < P; q += blockDim.x) {
+            const unsigned long long* row = pre + ((size_t)q * F + f) * NB * C;
+            const long long below = (long long)row[(size_t)b * C], all = (long long)row[(size_t)(NB - 1) * C];
+            dsum[2 * q] = __dmul_rn((double)below, inv);
+            dsum[2 * q + 1] = __dmul_rn((double)(all - below), inv);
+        }
+        __syncthreads();
+        for (int r = tid; r < n2; r += blockDim.x) {  // rows sum to zero: exact integer diagonal
+            double s = 0.0;
+            for (int c = 0; c < n2; ++c) s = __dadd_rn(s, ws[(size_t)r * n2 + c]);
+            ws[(size_t)r * n2 + r] = -s;
+        }
+        __syncthreads();
+        pw_leaf_values_block(ws, dsum, n2, l2, lv, A, y, x, &s_flag);
+        for (int xr = tid; xr < n2; xr += blockDim.x) {
+            double sub = 0.0;
+            for (int yc = 0; yc < n2; ++yc) sub = __dadd_rn(sub, __dmul_rn(lv[yc], ws[(size_t)xr * n2 + yc]));
+            term[xr] = __dmul_rn(lv[xr], __dsub_rn(dsum[xr], __dmul_rn(0.5, sub)));
+        }
+        __syncthreads();
+        if (tid == 0) {
+            double outer = 0.0;
+            for (int xr = 0; xr < n2; ++xr) outer = __dadd_rn(outer, term[xr]);
+            scores[k] = outer;
+        }
+        __syncthreads();
+    }
+}
+
+// The leaf pair-weight matrix of the grown tree (compute_pairwise_weight_sums,
+// pairwise_leaves.rs:51-91): integer counts, exact in any order.
+__global__ void rk_pairleafw_kernel(int64_t n_pairs, int L, const int64_t* __restrict__ pw,
+                                    const int64_t* __restrict__ pl, const uint16_t* __restrict__ leaf,
+                                    int32_t* __restrict__ wsum) {
+    for (int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < n_pairs; k += (int64_t)gridDim.x * blockDim.x) {
+        const int wl = leaf[pw[k]], ll = leaf[pl[k]];
+        if (wl == ll || wl >= L || ll >= L) continue;
+        atomicSub(&wsum[(size_t)wl * L + ll], 1);
+        atomicSub(&wsum[(size_t)ll * L + wl], 1);
+        atomicAdd(&wsum[(size_t)wl * L + wl], 1);
+        atomicAdd(&wsum[(size_t)ll * L + ll], 1);
+    }
+}
+
+// Cholesky pairwise leaves (compute_pairwise_leaf_deltas, pairwise_leaves.rs:
+// 219-242) from the leaf der sums (rk_leafsum_kernel's channel 0) with the raw
+// l2, one block; the seam gets these deltas, the approximant
+// normalize_leaf_values' document-weighted centring x lr (boosting.rs:
+// 2844-2880).  scratch: pw_scratch_doubles(L).
+__global__ void __launch_bounds__(kPwThreads)
+rk_pairleaf_kernel(int L, const int32_t* __restrict__ wsum, const unsigned long long* __restrict__ sums,
+                   const McState* __restrict__ ms, double l2, double lr, double* __restrict__ scratch,
+                   double* __restrict__ leaf_raw, double* __restrict__ leaf_lrv) {
+    __shared__ int s_flag;
+    const int m = L - 1, tid = threadIdx.x;
+    const double inv = ldexp(1.0, -ms->leaf_shift);
+    double* w = scratch;
+    double* A = w + (size_t)L * L;
+    double* der = A + (size_t)(m > 0 ? m : 1) * (m > 0 ? m : 1);
+    double* y = der + L;
+    double* x = y + L;
+    for (int k = tid; k < L * L; k += blockDim.x) w[k] = (double)wsum[k];
+    for (int q = tid; q < L; q += blockDim.x) der[q] = __dmul_rn((double)(long long)sums[3 * q], inv);
+    __syncthreads();
+    pw_leaf_values_block(w, der, L, l2, leaf_raw, A, y, x, &s_flag);
+    if (tid != 0) return;
+    double total = 0.0;
+    for (int q = 0; q < L; ++q) total = __dadd_rn(total, __dmul_rn((double)(long long)sums[3 * q + 2], inv));
+    double avg = 0.0;
+    const bool centre = fabs(total) > 1e-9;
+    if (centre) {
+        double acc = 0.0;
+        for (int q = 0; q < L; ++q)
+            acc = __dadd_rn(acc, __dmul_rn(leaf_raw[q], __dmul_rn((double)(long long)sums[3 * q + 2], inv)));
+        avg = __ddiv_rn(acc, total);
+    }
+    for (int q = 0; q < L; ++q) {
+        double v = leaf_raw[q];
+        if (centre) {
+            const double wq = __dmul_rn((double)(long long)sums[3 * q + 2], inv);
+            v = fabs(wq) > 1e-9 ? __dsub_rn(v, avg) : 0.0;
+        }
+        leaf_lrv[q] = __dmul_rn(v, lr);
+    }
+}
+
 unsigned grid_for(int64_t n, int threads = kMcThreads) {
     int64_t b = (n + threads - 1) / threads;
     if (b > 148 * 16) b = 148 * 16;
@@ -663,13 +957,24 @@ struct cbgpu_multi_session {
     void* leaf_export = nullptr;
     size_t hist_cells = 0;
     // ranking mode (grouped losses, K = 1)
-    int rank_mode = -1;  // -1: MultiClass; kRankQueryRmse / kRankPairLogit
+    int rank_mode = -1;  // -1: MultiClass; kRankQueryRmse / kRankPairLogit / kRankPairLogitPairwise
     int n_groups = 0;
     int64_t *d_goff = nullptr, *d_cstart = nullptr, *d_closer = nullptr;
     double *d_eff = nullptr, *d_der2 = nullptr, *d_tgt = nullptr;
+    // PairLogitPairwise: winner per competitor slot (losers are d_closer),
+    // the level's pair statistics, the leaf pair-weight matrix, scratch
+    int64_t n_pairs = 0;
+    int64_t* d_pwin = nullptr;
+    int32_t *d_pstat = nullptr, *d_pwsum = nullptr;
+    double* d_pwscratch = nullptr;
+    double raw_l2 = 0.0;
 
     ~cbgpu_multi_session() {
         if (st) cudaStreamSynchronize(st);
+        cudaFree(d_pwin);
+        cudaFree(d_pstat);
+        cudaFree(d_pwsum);
+        cudaFree(d_pwscratch);
         cudaFree(d_goff);
         cudaFree(d_cstart);
         cudaFree(d_closer);
@@ -874,7 +1179,7 @@ int cbgpu_multi_begin_raw(const cbgpu_begin_args* a, int32_t approx_dim, const f
 }
 
 int cbgpu_rank_begin_raw(const cbgpu_begin_args* a, const int64_t* group_offsets, int32_t n_groups,
-                         const int64_t* pair_winner, const int64_t* pair_loser, int64_t n_pairs,
+                         const int64_t* pair_winner, const int64_t* pair_loser, int64_t n_pairs, double l2_leaf_reg,
                          const float* const* float_columns, const double* borders_flat, const int32_t* border_counts,
                          cbgpu_multi_session** out) {
     if (!out) return mfail(CBGPU_ERR_INVALID, "rank_begin: out is NULL");
@@ -885,7 +1190,8 @@ int cbgpu_rank_begin_raw(const cbgpu_begin_args* a, const int64_t* group_offsets
     int mode;
     if (a->loss == CBGPU_LOSS_QUERYRMSE) mode = kRankQueryRmse;
     else if (a->loss == CBGPU_LOSS_PAIRLOGIT) mode = kRankPairLogit;
-    else return mfail(CBGPU_DECLINED, "rank_begin: loss %d is not QueryRMSE / PairLogit", a->loss);
+    else if (a->loss == CBGPU_LOSS_PAIRLOGIT_PAIRWISE) mode = kRankPairLogitPairwise;
+    else return mfail(CBGPU_DECLINED, "rank_begin: loss %d is not QueryRMSE / PairLogit / PairLogitPairwise", a->loss);
     if (a->grow_policy != CBGPU_GROW_SYMMETRIC || !a->boosting_type_is_plain || a->fold_count != 1)
         return mfail(CBGPU_DECLINED, "rank_begin: only Plain SymmetricTree with one fold");
     if (a->score_function != CBGPU_SCORE_COSINE && a->score_function != CBGPU_SCORE_L2)
@@ -895,6 +1201,23 @@ int cbgpu_rank_begin_raw(const cbgpu_begin_args* a, const int64_t* group_offsets
     if (a->world_size != 1) return mfail(CBGPU_DECLINED, "rank_begin: one GPU per ranking session");
     if (a->depth < 1 || a->depth > kMcMaxDepth)
         return mfail(CBGPU_DECLINED, "rank_begin: depth %d outside 1..%d", a->depth, kMcMaxDepth);
+    if (mode == kRankPairLogitPairwise) {
+        if (a->depth > kPwMaxDepth)
+            return mfail(CBGPU_DECLINED, "rank_begin: pairwise scoring covers depth 1..%d, got %d", kPwMaxDepth,
+                         a->depth);
+        if (!(l2_leaf_reg >= 0.0) || !std::isfinite(l2_leaf_reg))
+            return mfail(CBGPU_ERR_INVALID, "rank_begin: l2_leaf_reg must be finite and >= 0");
+        if (n_pairs >= ((int64_t)1 << 31) || a->n_features > 65535)
+            return mfail(CBGPU_DECLINED, "rank_begin: pairwise scoring counts pairs in int32 and features in "
+                                         "gridDim.y");
+        int maxb = 0;
+        for (int f = 0; f < a->n_features; ++f) maxb = std::max(maxb, (int)border_counts[f]);
+        const size_t P = (size_t)1 << (a->depth - 1);
+        const size_t bytes = (size_t)a->n_features * P * P * (size_t)(maxb + 1) * 2 * sizeof(int32_t);
+        if (bytes > kPwMaxStatBytes)
+            return mfail(CBGPU_DECLINED, "rank_begin: pair statistics need %zu bytes (> %zu)", bytes,
+                         kPwMaxStatBytes);
+    }
     const int64_t n = a->n;
     if (n < 1 || n > (int64_t)65535 * kMcChunk || a->n_features < 1)
         return mfail(CBGPU_ERR_INVALID, "rank_begin: bad n / n_features");
@@ -924,7 +1247,8 @@ int cbgpu_rank_begin_raw(const cbgpu_begin_args* a, const int64_t* group_offsets
     // (calc_pairwise_weights, boosting.rs:1761-1780)
     std::vector<int64_t> cstart((size_t)n + 1, 0), closer((size_t)std::max<int64_t>(n_pairs, 1));
     std::vector<double> eff((size_t)n, 0.0);
-    if (mode == kRankPairLogit) {
+    std::vector<int64_t> win;
+    if (mode != kRankQueryRmse) {
         for (int64_t k = 0; k < n_pairs; ++k) {
             const int64_t wv = pair_winner[k], lv = pair_loser[k];
             if (wv < 0 || wv >= n || lv < 0 || lv >= n || group_of[(size_t)wv] != group_of[(size_t)lv])
@@ -935,6 +1259,9 @@ int cbgpu_rank_begin_raw(const cbgpu_begin_args* a, const int64_t* group_offsets
         for (int64_t i = 0; i < n; ++i) cstart[(size_t)i + 1] += cstart[(size_t)i];
         std::vector<int64_t> fill(cstart.begin(), cstart.end() - 1);
         for (int64_t k = 0; k < n_pairs; ++k) closer[(size_t)fill[(size_t)pair_winner[k]]++] = pair_loser[k];
+        win.assign(closer.size(), 0);
+        for (int64_t i = 0; i < n; ++i)
+            for (int64_t k = cstart[(size_t)i]; k < cstart[(size_t)i + 1]; ++k) win[(size_t)k] = i;
         for (int g = 0; g < n_groups; ++g)
             for (int64_t wi = group_offsets[g]; wi < group_offsets[g + 1]; ++wi)
                 for (int64_t k = cstart[(size_t)wi]; k < cstart[(size_t)wi + 1]; ++k) {
@@ -958,6 +1285,22 @@ int cbgpu_rank_begin_raw(const cbgpu_begin_args* a, const int64_t* group_offsets
         if (!rc) rc = mdalloc(&s->d_eff, (size_t)n);
         if (!rc) rc = mdalloc(&s->d_der2, (size_t)n);
         if (!rc) rc = mdalloc(&s->d_tgt, (size_t)n);
+        if (!rc && mode == kRankPairLogitPairwise) {
+            const int L = 1 << a->depth, P = L / 2;
+            s->n_pairs = n_pairs;
+            s->raw_l2 = l2_leaf_reg;
+            const size_t leaf_scratch = pw_scratch_doubles(L);
+            const size_t score_scratch = L > kPwSmemMaxN2 ? (size_t)kPwGlobalBlocks * pw_scratch_doubles(L) : 0;
+            rc = mdalloc(&s->d_pwin, win.size());
+            if (!rc) rc = mdalloc(&s->d_pstat, (size_t)a->n_features * P * P * s->NB * 2);
+            if (!rc) rc = mdalloc(&s->d_pwsum, (size_t)L * L);
+            if (!rc) rc = mdalloc(&s->d_pwscratch, std::max(leaf_scratch, score_scratch));
+            const size_t smem = pw_scratch_doubles(std::min(L, kPwSmemMaxN2)) * sizeof(double);
+            if (!rc && smem > 48 * 1024 &&
+                cudaFuncSetAttribute(rk_pairscore_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+                    cudaSuccess)
+                rc = mfail(CBGPU_ERR_CUDA, "rank_begin: pairwise scorer shared memory (%zu bytes)", smem);
+        }
     }
     if (!rc) {
         cudaError_t e = cudaMemcpy(s->d_goff, group_offsets, sizeof(int64_t) * ((size_t)n_groups + 1),
@@ -967,6 +1310,8 @@ int cbgpu_rank_begin_raw(const cbgpu_begin_args* a, const int64_t* group_offsets
         if (e == cudaSuccess)
             e = cudaMemcpy(s->d_closer, closer.data(), sizeof(int64_t) * closer.size(), cudaMemcpyHostToDevice);
         if (e == cudaSuccess) e = cudaMemcpy(s->d_eff, eff.data(), sizeof(double) * (size_t)n, cudaMemcpyHostToDevice);
+        if (e == cudaSuccess && s->d_pwin)
+            e = cudaMemcpy(s->d_pwin, win.data(), sizeof(int64_t) * win.size(), cudaMemcpyHostToDevice);
         if (e != cudaSuccess) rc = mfail(CBGPU_ERR_CUDA, "rank_begin: upload failed: %s", cudaGetErrorString(e));
     }
     if (rc) {
@@ -1065,6 +1410,7 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
     mc_pack_kernel<<<g, kMcThreads, 0, st>>>(n, K, s->wd1, hw, s_mode, s->sw32, s->sw64, s->d_ms, s->q);
     MCU(cudaGetLastError());
     const unsigned chunks = (unsigned)((n + kMcChunk - 1) / kMcChunk);
+    const bool pairwise = s->rank_mode == kRankPairLogitPairwise;
     for (int l = 0; l < D; ++l) {
         const int leaves = 1 << l;
         const size_t cells = (size_t)leaves * F * NB * C;
@@ -1073,12 +1419,28 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
         const int use_smem = tab <= kMcSmemTable ? 1 : 0;
         if (use_smem && tab > 48 * 1024)
             MCU(cudaFuncSetAttribute(mc_hist_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tab));
-        mc_hist_kernel<<<dim3((unsigned)F, (unsigned)C, chunks), kMcThreads, use_smem ? tab : 0, st>>>(
-            n, F, NB, C, leaves, s->bins_fm, s->q, s->leaf, s->hist, use_smem);
+        // the pairwise scorer reads only the der channel
+        mc_hist_kernel<<<dim3((unsigned)F, pairwise ? 1u : (unsigned)C, chunks), kMcThreads, use_smem ? tab : 0,
+                         st>>>(n, F, NB, C, leaves, s->bins_fm, s->q, s->leaf, s->hist, use_smem);
         MCU(cudaGetLastError());
         mc_prefix_kernel<<<grid_for((int64_t)leaves * F * C), kMcThreads, 0, st>>>(leaves, F, NB, C, s->hist);
-        mc_score_kernel<<<grid_for((int64_t)F * NB), kMcThreads, 0, st>>>(leaves, F, NB, K, s->hist, s->d_bc, s->d_ms,
-                                                                          s->l2, s->score_fn, s->scores);
+        if (pairwise) {
+            const int64_t rows = (int64_t)F * leaves * leaves * 2;
+            MCU(cudaMemsetAsync(s->d_pstat, 0, sizeof(int32_t) * (size_t)rows * NB, st));
+            rk_pairstat_kernel<<<dim3(grid_for(s->n_pairs), (unsigned)F), kMcThreads, 0, st>>>(
+                s->n_pairs, n, leaves, NB, s->d_pwin, s->d_closer, s->bins_fm, s->leaf, s->d_pstat);
+            rk_pairprefix_kernel<<<grid_for(rows), kMcThreads, 0, st>>>(rows, NB, s->d_pstat);
+            const int n2 = 2 * leaves;
+            const int pw_smem = n2 <= kPwSmemMaxN2 ? 1 : 0;
+            const int64_t cand = (int64_t)F * NB;
+            const int64_t blocks = std::min<int64_t>(cand, pw_smem ? (int64_t)148 * 8 : (int64_t)kPwGlobalBlocks);
+            rk_pairscore_kernel<<<(unsigned)blocks, kPwThreads, pw_smem ? pw_scratch_doubles(n2) * sizeof(double) : 0,
+                                  st>>>(leaves, F, NB, C, s->hist, s->d_pstat, s->d_bc, s->d_ms, s->raw_l2, pw_smem,
+                                        s->d_pwscratch, s->scores);
+        } else {
+            mc_score_kernel<<<grid_for((int64_t)F * NB), kMcThreads, 0, st>>>(leaves, F, NB, K, s->hist, s->d_bc,
+                                                                              s->d_ms, s->l2, s->score_fn, s->scores);
+        }
         mc_argmax_kernel<<<1, 1024, 0, st>>>((int64_t)F * NB, NB, s->scores, l, s->d_ms);
         mc_route_kernel<<<g, kMcThreads, 0, st>>>(n, l, s->bins_fm, s->d_ms, s->leaf);
         MCU(cudaGetLastError());
@@ -1089,8 +1451,16 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
         rk_leafshift_kernel<<<1, 1, 0, st>>>(n, s->d_ms);
         MCU(cudaMemsetAsync(s->sums, 0, sizeof(unsigned long long) * 3 * (size_t)L, st));
         rk_leafsum_kernel<<<g, kMcThreads, 0, st>>>(n, L, s->wd1, s->d_der2, s->weight, s->leaf, s->sums, s->d_ms);
-        rk_newton_kernel<<<1, 1, 0, st>>>(L, s->rank_mode == kRankPairLogit ? 1 : 0, s->sums, s->d_ms, s->l2, s->lr,
-                                          s->leaf_raw, s->leaf_lrv);
+        if (pairwise) {
+            MCU(cudaMemsetAsync(s->d_pwsum, 0, sizeof(int32_t) * (size_t)L * L, st));
+            rk_pairleafw_kernel<<<grid_for(s->n_pairs), kMcThreads, 0, st>>>(s->n_pairs, L, s->d_pwin, s->d_closer,
+                                                                            s->leaf, s->d_pwsum);
+            rk_pairleaf_kernel<<<1, kPwThreads, 0, st>>>(L, s->d_pwsum, s->sums, s->d_ms, s->raw_l2, s->lr,
+                                                         s->d_pwscratch, s->leaf_raw, s->leaf_lrv);
+        } else {
+            rk_newton_kernel<<<1, 1, 0, st>>>(L, s->rank_mode == kRankPairLogit ? 1 : 0, s->sums, s->d_ms, s->l2,
+                                              s->lr, s->leaf_raw, s->leaf_lrv);
+        }
         MCU(cudaGetLastError());
     } else {
         // leaf values from the unsampled channels (boosting.rs:2610-2700)

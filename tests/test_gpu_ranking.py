@@ -1,10 +1,13 @@
-"""The grouped-loss (QueryRMSE, PairLogit) device mode against upstream and the oracle.
+"""The grouped-loss (QueryRMSE, PairLogit, PairLogitPairwise) device mode against upstream and the oracle.
 
 The device mode (csrc/multi.cu, cbgpu_rank_begin_raw) reproduces cb-train's
 grouped CPU branch: grouped ders (crates/cb-compute/src/ranking_der.rs),
 PairLogit's pairwise histogram weights (boosting.rs:1761-1780), Newton leaves
-and the PairLogit leaf centring (boosting.rs:2844-2880).  Trees must equal the
-oracle's; leaf values and staged approximants within the reference's 1e-5 bar.
+and the pair-loss leaf centring (boosting.rs:2844-2880); PairLogitPairwise
+scores splits with the pairwise scorer (crates/cb-compute/src/
+pairwise_scoring.rs) and takes Cholesky pairwise leaves
+(crates/cb-train/src/pairwise_leaves.rs).  Trees must equal the oracle's;
+leaf values and staged approximants within the reference's 1e-5 bar.
 """
 import json
 import os
@@ -30,7 +33,7 @@ def cb():
     return cb
 
 
-@pytest.mark.parametrize("loss", ["QueryRMSE", "PairLogit"])
+@pytest.mark.parametrize("loss", ["QueryRMSE", "PairLogit", "PairLogitPairwise"])
 def test_ranking_fixture(cb, loss):
     z = np.load(GOLDEN)
     p = json.loads(str(z[f"{loss}__params"]))
@@ -88,6 +91,26 @@ def test_ranking_matches_oracle(cb, loss, depth, score):
     assert np.max(np.abs(m.staged - o.staged)) <= TOL
 
 
+# depth 3 and 6 keep every level's pair-weight system in shared memory (2P <= 64);
+# depth 7 scores its last level from the global scratch slots
+@pytest.mark.parametrize("depth,n_groups", [(3, 60), (6, 120), (7, 40)])
+def test_pairwise_matches_oracle(cb, depth, n_groups):
+    X, y, offsets, pairs = _ranking_data(n_groups, 8, 40 + depth)
+    F = X.shape[1]
+    borders = [oracle.select_borders(X[:, f], 32) for f in range(F)]
+    fp = cb.FitParams(loss="PairLogitPairwise", depth=depth, iterations=3, learning_rate=0.3, l2_leaf_reg=3.0,
+                      boost_from_average=False)
+    m = cb.fit_ranking([X[:, f].copy() for f in range(F)], borders, y, offsets, fp, pairs=pairs, staged=True)
+    bins = oracle.quantize(X.T.copy(), borders)
+    o = oracle.train_ranking(bins, [len(b) for b in borders], y, offsets, loss="PairLogitPairwise", pairs=pairs,
+                             depth=depth, iterations=3, learning_rate=0.3, l2_leaf_reg=3.0)
+    np.testing.assert_array_equal(m.split_feature, o.split_feature)
+    np.testing.assert_array_equal(m.split_bin, o.split_bin)
+    assert np.max(np.abs(m.raw_leaf_values - o.raw_leaf_values)) <= TOL
+    assert np.max(np.abs(m.leaf_values - o.leaf_values)) <= TOL
+    assert np.max(np.abs(m.staged - o.staged)) <= TOL
+
+
 def test_ranking_declines_and_errors(cb):
     from catboost_rs_b200 import CbGpuError
     X, y, offsets, pairs = _ranking_data(20, 4, 3)
@@ -106,6 +129,10 @@ def test_ranking_declines_and_errors(cb):
     assert not ok and rt.decline_reason
     rt, ok = begin(loss="RMSE")
     assert not ok
+    rt = cb.B200MultiRuntime()  # the pairwise scorer covers depth 1..8
+    ok = rt.begin_ranking_raw("PairLogitPairwise", 9, True, 1, "Cosine", cols, borders, None, n, F, nb, 0.3, 3.0,
+                              cb.DeviceTrainConfig(), offsets, pairs, l2_leaf_reg=3.0)
+    assert not ok and "depth" in rt.decline_reason
     with pytest.raises(CbGpuError, match="crosses group"):
         begin(prs=np.array([[0, int(offsets[1])]]))  # winner and loser in different groups
     with pytest.raises(CbGpuError, match="group offsets"):
