@@ -1,7 +1,7 @@
 /*
  * cb_oracle_rank.c -- CPU restatement of catboost_rs's grouped (ranking)
- * losses on the oblivious loop: QueryRMSE and PairLogit on pointwise
- * histograms, and PairLogitPairwise with the pairwise split scoring and
+ * losses on the oblivious loop: QueryRMSE, QuerySoftMax and PairLogit on
+ * pointwise histograms, and PairLogitPairwise with the pairwise split scoring and
  * Cholesky leaves (crates/cb-compute/src/ranking_der.rs, pairwise_scoring.rs,
  * crates/cb-train/src/boosting.rs grouped branch, pairwise_leaves.rs,
  * tree.rs:3740-3960, query_info.rs).
@@ -14,14 +14,19 @@
  *     QueryRMSE der1 = ((t - a) - queryAvrg) * w, der2 = -w with
  *     queryAvrg = sum((t - a) * w) / sum(w) per group; PairLogit scatters
  *     w_pair * p (p = e^loser / (e^loser + e^winner)) doc-ascending,
- *     competitor-order;  the ders already carry the weights;
+ *     competitor-order; QuerySoftMax (ranking_der.rs:247-320, loss.rs:608-619)
+ *     takes p = e^(beta (a - max)) w / sum over the group (max over w > 0),
+ *     der1 = beta (-sumWT p + w t), der2 = beta sumWT (beta p (p - 1) - lambda)
+ *     with sumWT = sum(w t) over w > 0, t > 0 (ders 0 when sumWT <= 0 or
+ *     w <= 0);  the ders already carry the weights;
  *  2. the histogram weight channel: PairLogit uses the pairwise weights
  *     (calc_pairwise_weights, boosting.rs:1761-1780), QueryRMSE the object
  *     weights;
  *  3. the scalar greedy search;
  *  4. Newton leaves sum(der1) / (-sum(der2) + scaled_l2) over unit leaf
  *     weights (boosting.rs:8330-8400, leaf.rs:223-232), scaled_l2 from the
- *     object-weight sum;
+ *     object-weight sum; QuerySoftMax takes Gradient leaves over the same unit
+ *     weights, sum(der1) / (count + scaled_l2) (leaf.rs:161-194);
  *  5. normalize_leaf_values (boosting.rs:2844-2880): PairLogit subtracts the
  *     document-weighted mean leaf value, then x lr (f32-narrowed).
  * PairLogitPairwise replaces 3-4: per level and feature the der sums
@@ -32,6 +37,7 @@
  */
 #include "cb_oracle.h"
 
+#include <float.h>
 #include <math.h>
 #include <stdlib.h>
 #include <string.h>
@@ -324,7 +330,28 @@ int orc_train_ranking(const orc_rank_args* a, orc_rank_out* o) {
         for (int32_t g = 0; g < a->n_groups; ++g) {
             const int64_t b = a->group_offsets[g], e = a->group_offsets[g + 1];
             if (e <= b) continue;
-            if (a->loss == ORC_RANK_QUERYRMSE) {
+            if (a->loss == ORC_RANK_QUERYSOFTMAX) {
+                const double beta = a->softmax_beta, lambda = a->softmax_lambda;
+                double max_a = -DBL_MAX;
+                int64_t nt = 0;
+                for (int64_t i = b; i < e; ++i)
+                    if (w[i] > 0.0) {
+                        if (approx[i] > max_a) max_a = approx[i];
+                        if (a->target[i] > 0.0) tmp[nt++] = w[i] * a->target[i];
+                    }
+                const double swt = orc_sum_f64(tmp, nt);
+                if (swt > 0.0) {
+                    for (int64_t i = b; i < e; ++i) tmp[i - b] = exp(beta * (approx[i] - max_a)) * w[i];
+                    const double sum_exp = orc_sum_f64(tmp, e - b);
+                    for (int64_t i = b; i < e; ++i) {
+                        if (w[i] > 0.0 && sum_exp > 0.0) {
+                            const double p = tmp[i - b] / sum_exp;
+                            d2[i] = beta * swt * (beta * p * (p - 1.0) - lambda);
+                            d1[i] = beta * (-swt * p + w[i] * a->target[i]);
+                        }
+                    }
+                }
+            } else if (a->loss == ORC_RANK_QUERYRMSE) {
                 for (int64_t i = b; i < e; ++i) tmp[i - b] = (a->target[i] - approx[i]) * w[i];
                 double num = orc_sum_f64(tmp, e - b);
                 double den = orc_sum_f64(w + b, e - b);
@@ -376,20 +403,26 @@ int orc_train_ranking(const orc_rank_args* a, orc_rank_out* o) {
         }
         const int32_t nl = 1 << taken;
         /* 4. Newton leaves over unit leaf weights, ordered per-leaf sums */
-        double* sd = (double*)calloc((size_t)nl * 3, sizeof(double));
+        double* sd = (double*)calloc((size_t)nl * 4, sizeof(double));
         for (int64_t i = 0; i < n; ++i) {
-            sd[3 * leaf[i]] += d1[i];
-            sd[3 * leaf[i] + 1] += d2[i] * 1.0;
-            sd[3 * leaf[i] + 2] += w[i];
+            sd[4 * leaf[i]] += d1[i];
+            sd[4 * leaf[i] + 1] += d2[i] * 1.0;
+            sd[4 * leaf[i] + 2] += w[i];
+            sd[4 * leaf[i] + 3] += 1.0;
         }
         for (int32_t q = 0; q < L; ++q) {
             lv[q] = 0.0;
             lw[q] = 0.0;
         }
         for (int32_t q = 0; q < nl; ++q) {
-            const double den = -sd[3 * q + 1] + scaled_l2;
-            lv[q] = den == 0.0 ? 0.0 : sd[3 * q] / den;
-            lw[q] = sd[3 * q + 2];
+            if (a->loss == ORC_RANK_QUERYSOFTMAX) {
+                const double cnt = sd[4 * q + 3];
+                lv[q] = cnt > 0.0 ? sd[4 * q] / (cnt + scaled_l2) : 0.0;
+            } else {
+                const double den = -sd[4 * q + 1] + scaled_l2;
+                lv[q] = den == 0.0 ? 0.0 : sd[4 * q] / den;
+            }
+            lw[q] = sd[4 * q + 2];
         }
         free(sd);
         if (a->loss == ORC_RANK_PAIRLOGIT_PAIRWISE) {

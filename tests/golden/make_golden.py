@@ -234,7 +234,7 @@ def multiclass_fixture(ref):
 
 
 def ranking_fixtures(ref):
-    """Upstream QueryRMSE / PairLogit / PairLogitPairwise fixtures on the reference's frozen ranking
+    """Upstream QueryRMSE / PairLogit / PairLogitPairwise / QuerySoftMax fixtures on the reference's frozen ranking
     corpus (12 objects, 5 contiguous groups, 7 explicit pairs): inputs, group
     offsets, pairs, and per loss the trees, leaf values and staged approximants."""
     fx = os.path.join(ref, "crates/cb-oracle/fixtures/ranking_corpus")
@@ -244,12 +244,14 @@ def ranking_fixtures(ref):
                   y=np.load(os.path.join(fx, "inputs/y.npy")).astype(np.float64), group_offsets=offsets,
                   pairs=np.load(os.path.join(fx, "inputs/pairs.npy")).astype(np.int64))
     losses = []
-    for loss in ("QueryRMSE", "PairLogit", "PairLogitPairwise"):
+    for loss in ("QueryRMSE", "PairLogit", "PairLogitPairwise", "QuerySoftMax"):
         cfg = json.loads(_read(os.path.join(fx, loss, "config.json")))
         model = json.loads(_read(os.path.join(fx, loss, "model.json")))
         mparams = model["model_info"].get("params")
         mparams = json.loads(mparams) if isinstance(mparams, str) else (mparams or {})
-        l2 = float(mparams.get("tree_learner_options", {}).get("l2_leaf_reg", 3.0))
+        tlo = mparams.get("tree_learner_options", {})
+        l2 = float(tlo.get("l2_leaf_reg", 3.0))
+        lf = mparams.get("loss_function", {}).get("params", {})
         trees = model["oblivious_trees"]
         arrays[f"{loss}__split_feature"] = np.array([[s["float_feature_index"] for s in t["splits"]] for t in trees],
                                                     dtype=np.int32)
@@ -259,7 +261,8 @@ def ranking_fixtures(ref):
         arrays[f"{loss}__params"] = np.array(json.dumps({
             "depth": int(cfg["depth"]), "iterations": int(cfg["iterations"]),
             "learning_rate": float(cfg["learning_rate"]), "l2_leaf_reg": l2,
-            "random_seed": int(cfg["random_seed"])}))
+            "random_seed": int(cfg["random_seed"]), "leaf_estimation_method": tlo.get("leaf_estimation_method"),
+            "softmax_lambda": float(lf.get("lambda", 0.01)), "softmax_beta": float(lf.get("beta", 1.0))}))
         losses.append(loss)
     np.savez_compressed(os.path.join(OUT, "ranking_corpus.npz"), **arrays)
     return ["ranking_corpus/" + l for l in losses]

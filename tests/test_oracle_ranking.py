@@ -1,9 +1,11 @@
-"""Pin the oracle's grouped-loss loop (QueryRMSE, PairLogit, PairLogitPairwise) to upstream.
+"""Pin the oracle's grouped-loss loop (QueryRMSE, PairLogit, PairLogitPairwise, QuerySoftMax) to upstream.
 
 tests/golden/ranking_corpus.npz comes from the reference's frozen ranking
 corpus (crates/cb-oracle/fixtures/ranking_corpus: 12 objects in 5 contiguous
 groups, 7 explicit pairs, depth 2, 5 iterations, lr 0.3), which the
-reference's own ranking oracle tests train against.  PairLogitPairwise scores
+reference's own ranking oracle tests train against.  QuerySoftMax takes a
+per-group softmax der (crates/cb-compute/src/ranking_der.rs:247-320) and
+Gradient leaves (the fixture's leaf_estimation_method).  PairLogitPairwise scores
 splits with the pairwise statistics and a per-candidate Cholesky solve
 (crates/cb-compute/src/pairwise_scoring.rs) and takes its leaves from the
 pairwise Cholesky system (crates/cb-train/src/pairwise_leaves.rs).  Trees are compared
@@ -33,11 +35,14 @@ def _fit(d, loss, borders, **kw):
     bins = oracle.quantize(d["X"].T.copy(), borders)
     args = dict(loss=loss, pairs=d["pairs"], depth=p["depth"], iterations=p["iterations"],
                 learning_rate=p["learning_rate"], l2_leaf_reg=p["l2_leaf_reg"], random_seed=p["random_seed"])
+    if loss == "QuerySoftMax":
+        assert p["leaf_estimation_method"] == "Gradient"
+        args.update(softmax_lambda=p["softmax_lambda"], softmax_beta=p["softmax_beta"])
     args.update(kw)
     return oracle.train_ranking(bins, [len(b) for b in borders], d["y"], d["group_offsets"], **args)
 
 
-@pytest.mark.parametrize("loss", ["QueryRMSE", "PairLogit", "PairLogitPairwise"])
+@pytest.mark.parametrize("loss", ["QueryRMSE", "PairLogit", "PairLogitPairwise", "QuerySoftMax"])
 @pytest.mark.parametrize("border_set", ["full", "model"])
 def test_ranking_matches_upstream(loss, border_set):
     d = _load()
