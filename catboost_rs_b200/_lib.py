@@ -15,6 +15,10 @@ LIB_PATH = os.path.join(HERE, "libcbgpu.so")
 OK, DECLINED, ERR_INVALID, ERR_CUDA, ERR_OOM, ERR_NCCL, ERR_DEVICE, ERR_NO_DEVICE = range(8)
 
 
+class RankParams(C.Structure):
+    _fields_ = [("l2_leaf_reg", C.c_double), ("softmax_lambda", C.c_double), ("softmax_beta", C.c_double)]
+
+
 class BeginArgs(C.Structure):
     _fields_ = [
         ("loss", C.c_int32), ("depth", C.c_int32), ("boosting_type_is_plain", C.c_int32),
@@ -86,8 +90,8 @@ def load(path: str = LIB_PATH):
         "cbgpu_multi_begin_raw": ([C.POINTER(BeginArgs), i32, vp, vp, vp, C.POINTER(vp)], C.c_int),
         "cbgpu_multi_grow_tree": ([vp, vp, vp, i64, vp, i64, vp, vp, vp, vp, vp, i32], C.c_int),
         "cbgpu_multi_approx": ([vp, vp, i64], C.c_int),
-        "cbgpu_rank_begin_raw": ([C.POINTER(BeginArgs), vp, i32, vp, vp, i64, C.c_double, vp, vp, vp, C.POINTER(vp)],
-                                 C.c_int),
+        "cbgpu_rank_begin_raw": ([C.POINTER(BeginArgs), vp, i32, vp, vp, i64, C.POINTER(RankParams), vp, vp, vp,
+                                  C.POINTER(vp)], C.c_int),
         "cbgpu_multi_end": ([vp], C.c_int),
         "cbgpu_nccl_unique_id": ([vp], C.c_int),
         "cbgpu_version": ([], C.c_char_p),

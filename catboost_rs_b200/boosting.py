@@ -30,6 +30,8 @@ class FitParams:
     bagging_temperature: float = 1.0
     random_seed: int = 0
     boost_from_average: bool = True
+    softmax_lambda: float = 0.01  # QuerySoftMax:lambda
+    softmax_beta: float = 1.0     # QuerySoftMax:beta
 
 
 @dataclass
@@ -232,10 +234,11 @@ def normalize_leaf_values(pairwise: bool, lr: float, leaf_weights, raw) -> np.nd
 def fit_ranking(float_columns: Sequence[np.ndarray], borders: Sequence[Sequence[float]], target, group_offsets,
                 params: FitParams, pairs=None, weights=None, *, staged: bool = False,
                 device: int = 0) -> RankingModel:
-    """QueryRMSE / PairLogit / PairLogitPairwise fit (params.loss) on raw f32
-    columns with fixed borders: cb-train's grouped loop (pointwise histograms
-    and Newton leaves, or pairwise scoring and Cholesky leaves) over the
-    device's ranking arm; leaf normalisation on the host as cb-train does it."""
+    """QueryRMSE / QuerySoftMax / PairLogit / PairLogitPairwise fit
+    (params.loss) on raw f32 columns with fixed borders: cb-train's grouped
+    loop (pointwise histograms with Newton or, for QuerySoftMax, Gradient
+    leaves; or pairwise scoring and Cholesky leaves) over the device's ranking
+    arm; leaf normalisation on the host as cb-train does it."""
     p = params
     cols = [np.ascontiguousarray(c, dtype=np.float32) for c in float_columns]
     F = len(cols)
@@ -249,7 +252,8 @@ def fit_ranking(float_columns: Sequence[np.ndarray], borders: Sequence[Sequence[
     rt = B200MultiRuntime()
     n_bins = max(len(b) for b in borders) + 1
     ok = rt.begin_ranking_raw(p.loss, p.depth, True, 1, p.score_function, cols, borders, w, n, F, n_bins, lr,
-                              scaled_l2, cfg, group_offsets, pairs, l2_leaf_reg=p.l2_leaf_reg)
+                              scaled_l2, cfg, group_offsets, pairs, l2_leaf_reg=p.l2_leaf_reg,
+                              softmax_lambda=p.softmax_lambda, softmax_beta=p.softmax_beta)
     if not ok:
         raise RuntimeError(f"device declined: {rt.decline_reason}")
     T, D = p.iterations, p.depth

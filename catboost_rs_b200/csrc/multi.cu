@@ -486,7 +486,7 @@ __global__ void mc_apply_pending_kernel(int64_t n, int K, int L, double* __restr
 
 // ---- ranking mode (grouped losses, K = 1) ----------------------------------
 
-enum : int { kRankQueryRmse = 0, kRankPairLogit = 1, kRankPairLogitPairwise = 2 };
+enum : int { kRankQueryRmse = 0, kRankPairLogit = 1, kRankPairLogitPairwise = 2, kRankQuerySoftMax = 3 };
 constexpr double kPairwisePrior = 0.1;  // PairwiseNonDiagReg default (oblivious_tree_options.cpp:16)
 
 // Grouped derivatives (calc_ders_for_queries, crates/cb-compute/src/
@@ -496,17 +496,48 @@ constexpr double kPairwisePrior = 0.1;  // PairwiseNonDiagReg default (oblivious
 //             der2 = -1 * w;
 //  PairLogit  doc-ascending winners, competitor order: p = e^l / (e^l + e^w),
 //             winner += p, loser -= p (der2: p * (p - 1)), pair weight 1.
+//  QuerySoftMax (ranking_der.rs:247-320, loss.rs:608-619): max approx and
+//             sumWT = sum(w t) over w > 0 (t > 0 terms), ew = e^(beta (a - max)) w,
+//             p = ew / sum(ew), der1 = beta (-sumWT p + w t),
+//             der2 = beta sumWT (beta p (p - 1) - lambda); 0 when sumWT <= 0 or w <= 0.
 // The ders carry the weights already (boosting.rs:7453-7490).
 __global__ void rk_der_kernel(int n_groups, int mode, const int64_t* __restrict__ goff,
                               const int64_t* __restrict__ cstart, const int64_t* __restrict__ closer,
                               const double* __restrict__ approx, const double* __restrict__ target,
-                              const double* __restrict__ weight, double* __restrict__ d1, double* __restrict__ d2,
-                              McState* __restrict__ ms) {
+                              const double* __restrict__ weight, double sm_lambda, double sm_beta,
+                              double* __restrict__ d1, double* __restrict__ d2, McState* __restrict__ ms) {
     const int g = blockIdx.x * blockDim.x + threadIdx.x;
     if (g >= n_groups) return;
     const int64_t b = goff[g], e = goff[g + 1];
     bool finite = true;
-    if (mode == kRankQueryRmse) {
+    if (mode == kRankQuerySoftMax) {
+        double mx = -DBL_MAX, swt = 0.0;
+        for (int64_t i = b; i < e; ++i) {
+            const double w = weight ? weight[i] : 1.0;
+            d1[i] = 0.0;
+            d2[i] = 0.0;
+            if (w > 0.0) {
+                if (approx[i] > mx) mx = approx[i];
+                if (target[i] > 0.0) swt = __dadd_rn(swt, __dmul_rn(w, target[i]));
+            }
+        }
+        if (swt > 0.0) {
+            double sum_exp = 0.0;
+            for (int64_t i = b; i < e; ++i)
+                sum_exp = __dadd_rn(sum_exp, __dmul_rn(exp(__dmul_rn(sm_beta, __dsub_rn(approx[i], mx))),
+                                                       weight ? weight[i] : 1.0));
+            for (int64_t i = b; i < e; ++i) {
+                const double w = weight ? weight[i] : 1.0;
+                if (!(w > 0.0 && sum_exp > 0.0)) continue;
+                const double ew = __dmul_rn(exp(__dmul_rn(sm_beta, __dsub_rn(approx[i], mx))), w);
+                const double p = __ddiv_rn(ew, sum_exp);
+                d2[i] = __dmul_rn(__dmul_rn(sm_beta, swt),
+                                  __dsub_rn(__dmul_rn(__dmul_rn(sm_beta, p), __dsub_rn(p, 1.0)), sm_lambda));
+                d1[i] = __dmul_rn(sm_beta, __dadd_rn(__dmul_rn(-swt, p), __dmul_rn(w, target[i])));
+            }
+        }
+        for (int64_t i = b; i < e; ++i) finite &= isfinite(d1[i]) && isfinite(d2[i]);
+    } else if (mode == kRankQueryRmse) {
         double num = 0.0, den = 0.0;
         for (int64_t i = b; i < e; ++i) {
             const double w = weight ? weight[i] : 1.0;
@@ -550,7 +581,7 @@ __global__ void rk_der_kernel(int n_groups, int mode, const int64_t* __restrict_
 // max |der1|, |der2|, |w| of the tree -> leaf_shift (sums over n rows < 2^62)
 __global__ void rk_leafmax_kernel(int64_t n, const double* __restrict__ d1, const double* __restrict__ d2,
                                   const double* __restrict__ weight, McState* __restrict__ ms) {
-    double mx = 0.0;
+    double mx = 1.0;  // the unit leaf weights Gradient leaves count
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
         mx = fmax(mx, fmax(fabs(d1[i]), fmax(fabs(d2[i]), fabs(weight ? weight[i] : 1.0))));
     for (int o = 16; o > 0; o >>= 1) mx = fmax(mx, __shfl_xor_sync(0xffffffffu, mx, o));
@@ -569,10 +600,11 @@ __global__ void rk_leafshift_kernel(int64_t n, McState* ms) {
 }
 
 // Per-leaf int64 sums of der1, der2 (unit leaf weights for Newton,
-// boosting.rs:8345-8380) and the object weight (normalize_leaf_values' leaf
-// weights, boosting.rs:8525-8540): sums[leaf][3].
+// boosting.rs:8345-8380) -- or, for Gradient leaves (count = 1), the row
+// count -- and the object weight (normalize_leaf_values' leaf weights,
+// boosting.rs:8525-8540): sums[leaf][3].
 __global__ void rk_leafsum_kernel(int64_t n, int L, const double* __restrict__ d1, const double* __restrict__ d2,
-                                  const double* __restrict__ weight, const uint16_t* __restrict__ leaf,
+                                  const double* __restrict__ weight, const uint16_t* __restrict__ leaf, int count,
                                   unsigned long long* __restrict__ sums, McState* __restrict__ ms) {
     __shared__ unsigned long long t3[3 * (1 << kMcMaxDepth)];
     for (int k = threadIdx.x; k < 3 * L; k += blockDim.x) t3[k] = 0ull;
@@ -585,7 +617,7 @@ __global__ void rk_leafsum_kernel(int64_t n, int L, const double* __restrict__ d
             continue;
         }
         atomicAdd(&t3[3 * q], (unsigned long long)llrint(ldexp(d1[i], sh)));
-        atomicAdd(&t3[3 * q + 1], (unsigned long long)llrint(ldexp(d2[i], sh)));
+        atomicAdd(&t3[3 * q + 1], (unsigned long long)llrint(ldexp(count ? 1.0 : d2[i], sh)));
         atomicAdd(&t3[3 * q + 2], (unsigned long long)llrint(ldexp(weight ? weight[i] : 1.0, sh)));
     }
     __syncthreads();
@@ -593,11 +625,12 @@ __global__ void rk_leafsum_kernel(int64_t n, int L, const double* __restrict__ d
         if (t3[k]) atomicAdd(&sums[k], t3[k]);
 }
 
-// Newton leaves sum(der1) / (-sum(der2) + scaled_l2) (leaf.rs:223-232); the
-// raw deltas go back through the seam; the approximant gets
-// normalize_leaf_values' result (PairLogit: minus the document-weighted mean,
-// boosting.rs:2844-2880) x lr.  One thread: L <= 1024 leaves.
-__global__ void rk_newton_kernel(int L, int pairwise, const unsigned long long* __restrict__ sums,
+// Newton leaves sum(der1) / (-sum(der2) + scaled_l2) (leaf.rs:223-232), or
+// Gradient leaves sum(der1) / (count + scaled_l2) (calc_average,
+// leaf.rs:161-194); the raw deltas go back through the seam; the approximant
+// gets normalize_leaf_values' result (PairLogit: minus the document-weighted
+// mean, boosting.rs:2844-2880) x lr.  One thread: L <= 1024 leaves.
+__global__ void rk_newton_kernel(int L, int pairwise, int gradient, const unsigned long long* __restrict__ sums,
                                  const McState* __restrict__ ms, double l2, double lr, double* __restrict__ leaf_raw,
                                  double* __restrict__ leaf_lrv) {
     if (blockIdx.x != 0 || threadIdx.x != 0) return;
@@ -605,8 +638,12 @@ __global__ void rk_newton_kernel(int L, int pairwise, const unsigned long long* 
     for (int q = 0; q < L; ++q) {
         const double s1 = __dmul_rn((double)(long long)sums[3 * q], inv);
         const double s2 = __dmul_rn((double)(long long)sums[3 * q + 1], inv);
-        const double den = __dadd_rn(-s2, l2);
-        leaf_raw[q] = den == 0.0 ? 0.0 : __ddiv_rn(s1, den);
+        if (gradient) {
+            leaf_raw[q] = s2 > 0.0 ? __ddiv_rn(s1, __dadd_rn(s2, l2)) : 0.0;
+        } else {
+            const double den = __dadd_rn(-s2, l2);
+            leaf_raw[q] = den == 0.0 ? 0.0 : __ddiv_rn(s1, den);
+        }
     }
     double avg = 0.0;
     bool centre = false;
@@ -968,6 +1005,7 @@ struct cbgpu_multi_session {
     int32_t *d_pstat = nullptr, *d_pwsum = nullptr;
     double* d_pwscratch = nullptr;
     double raw_l2 = 0.0;
+    double sm_lambda = 0.01, sm_beta = 1.0;
 
     ~cbgpu_multi_session() {
         if (st) cudaStreamSynchronize(st);
@@ -1179,8 +1217,8 @@ int cbgpu_multi_begin_raw(const cbgpu_begin_args* a, int32_t approx_dim, const f
 }
 
 int cbgpu_rank_begin_raw(const cbgpu_begin_args* a, const int64_t* group_offsets, int32_t n_groups,
-                         const int64_t* pair_winner, const int64_t* pair_loser, int64_t n_pairs, double l2_leaf_reg,
-                         const float* const* float_columns, const double* borders_flat, const int32_t* border_counts,
+                         const int64_t* pair_winner, const int64_t* pair_loser, int64_t n_pairs,
+                         const cbgpu_rank_params* params, const float* const* float_columns, const double* borders_flat, const int32_t* border_counts,
                          cbgpu_multi_session** out) {
     if (!out) return mfail(CBGPU_ERR_INVALID, "rank_begin: out is NULL");
     *out = nullptr;
@@ -1191,7 +1229,14 @@ int cbgpu_rank_begin_raw(const cbgpu_begin_args* a, const int64_t* group_offsets
     if (a->loss == CBGPU_LOSS_QUERYRMSE) mode = kRankQueryRmse;
     else if (a->loss == CBGPU_LOSS_PAIRLOGIT) mode = kRankPairLogit;
     else if (a->loss == CBGPU_LOSS_PAIRLOGIT_PAIRWISE) mode = kRankPairLogitPairwise;
-    else return mfail(CBGPU_DECLINED, "rank_begin: loss %d is not QueryRMSE / PairLogit / PairLogitPairwise", a->loss);
+    else if (a->loss == CBGPU_LOSS_QUERYSOFTMAX) mode = kRankQuerySoftMax;
+    else return mfail(CBGPU_DECLINED, "rank_begin: loss %d is not a covered grouped loss", a->loss);
+    const double l2_leaf_reg = params && params->l2_leaf_reg >= 0.0 ? params->l2_leaf_reg : a->scaled_l2;
+    const double sm_lambda = params ? params->softmax_lambda : 0.01;
+    const double sm_beta = params ? params->softmax_beta : 1.0;
+    if (mode == kRankQuerySoftMax && !(std::isfinite(sm_lambda) && sm_lambda >= 0.0 && std::isfinite(sm_beta) &&
+                                       sm_beta > 0.0))  // LossFunction validation (runtime.rs:698-715)
+        return mfail(CBGPU_ERR_INVALID, "rank_begin: QuerySoftMax needs lambda >= 0 and beta > 0, finite");
     if (a->grow_policy != CBGPU_GROW_SYMMETRIC || !a->boosting_type_is_plain || a->fold_count != 1)
         return mfail(CBGPU_DECLINED, "rank_begin: only Plain SymmetricTree with one fold");
     if (a->score_function != CBGPU_SCORE_COSINE && a->score_function != CBGPU_SCORE_L2)
@@ -1248,7 +1293,7 @@ int cbgpu_rank_begin_raw(const cbgpu_begin_args* a, const int64_t* group_offsets
     std::vector<int64_t> cstart((size_t)n + 1, 0), closer((size_t)std::max<int64_t>(n_pairs, 1));
     std::vector<double> eff((size_t)n, 0.0);
     std::vector<int64_t> win;
-    if (mode != kRankQueryRmse) {
+    if (mode == kRankPairLogit || mode == kRankPairLogitPairwise) {
         for (int64_t k = 0; k < n_pairs; ++k) {
             const int64_t wv = pair_winner[k], lv = pair_loser[k];
             if (wv < 0 || wv >= n || lv < 0 || lv >= n || group_of[(size_t)wv] != group_of[(size_t)lv])
@@ -1279,6 +1324,8 @@ int cbgpu_rank_begin_raw(const cbgpu_begin_args* a, const int64_t* group_offsets
     if (!rc) {
         s->rank_mode = mode;
         s->n_groups = n_groups;
+        s->sm_lambda = sm_lambda;
+        s->sm_beta = sm_beta;
         rc = mdalloc(&s->d_goff, (size_t)n_groups + 1);
         if (!rc) rc = mdalloc(&s->d_cstart, (size_t)n + 1);
         if (!rc) rc = mdalloc(&s->d_closer, closer.size());
@@ -1392,8 +1439,8 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
         if (s->pending)
             mc_apply_pending_kernel<<<g, kMcThreads, 0, st>>>(n, 1, L, s->approx, s->leaf, s->leaf_lrv);
         rk_der_kernel<<<(unsigned)((s->n_groups + 127) / 128), 128, 0, st>>>(
-            s->n_groups, s->rank_mode, s->d_goff, s->d_cstart, s->d_closer, s->approx, s->d_tgt, s->weight, s->wd1,
-            s->d_der2, s->d_ms);
+            s->n_groups, s->rank_mode, s->d_goff, s->d_cstart, s->d_closer, s->approx, s->d_tgt, s->weight,
+            s->sm_lambda, s->sm_beta, s->wd1, s->d_der2, s->d_ms);
     } else {
         mc_der_kernel<<<g, kMcThreads, 0, st>>>(n, K, s->approx, s->target, s->weight, s->leaf, s->leaf_lrv, L,
                                                 s->pending ? 1 : 0, s->wd1, s->d_ms);
@@ -1450,7 +1497,9 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
         rk_leafmax_kernel<<<g, kMcThreads, 0, st>>>(n, s->wd1, s->d_der2, s->weight, s->d_ms);
         rk_leafshift_kernel<<<1, 1, 0, st>>>(n, s->d_ms);
         MCU(cudaMemsetAsync(s->sums, 0, sizeof(unsigned long long) * 3 * (size_t)L, st));
-        rk_leafsum_kernel<<<g, kMcThreads, 0, st>>>(n, L, s->wd1, s->d_der2, s->weight, s->leaf, s->sums, s->d_ms);
+        const int gradient = s->rank_mode == kRankQuerySoftMax ? 1 : 0;
+        rk_leafsum_kernel<<<g, kMcThreads, 0, st>>>(n, L, s->wd1, s->d_der2, s->weight, s->leaf, gradient, s->sums,
+                                                    s->d_ms);
         if (pairwise) {
             MCU(cudaMemsetAsync(s->d_pwsum, 0, sizeof(int32_t) * (size_t)L * L, st));
             rk_pairleafw_kernel<<<grid_for(s->n_pairs), kMcThreads, 0, st>>>(s->n_pairs, L, s->d_pwin, s->d_closer,
@@ -1458,8 +1507,8 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
             rk_pairleaf_kernel<<<1, kPwThreads, 0, st>>>(L, s->d_pwsum, s->sums, s->d_ms, s->raw_l2, s->lr,
                                                          s->d_pwscratch, s->leaf_raw, s->leaf_lrv);
         } else {
-            rk_newton_kernel<<<1, 1, 0, st>>>(L, s->rank_mode == kRankPairLogit ? 1 : 0, s->sums, s->d_ms, s->l2,
-                                              s->lr, s->leaf_raw, s->leaf_lrv);
+            rk_newton_kernel<<<1, 1, 0, st>>>(L, s->rank_mode == kRankPairLogit ? 1 : 0, gradient, s->sums, s->d_ms,
+                                              s->l2, s->lr, s->leaf_raw, s->leaf_lrv);
         }
         MCU(cudaGetLastError());
     } else {

@@ -50,7 +50,8 @@ typedef enum {
  * declines them. */
 typedef enum {
     CBGPU_LOSS_RMSE = 0, CBGPU_LOSS_LOGLOSS = 1, CBGPU_LOSS_CROSSENTROPY = 2, CBGPU_LOSS_MULTICLASS = 3,
-    CBGPU_LOSS_QUERYRMSE = 4, CBGPU_LOSS_PAIRLOGIT = 5, CBGPU_LOSS_PAIRLOGIT_PAIRWISE = 6
+    CBGPU_LOSS_QUERYRMSE = 4, CBGPU_LOSS_PAIRLOGIT = 5, CBGPU_LOSS_PAIRLOGIT_PAIRWISE = 6,
+    CBGPU_LOSS_QUERYSOFTMAX = 7
 } cbgpu_loss;
 
 /* EScoreFunction (runtime.rs:834-864); Cosine is the default. */
@@ -280,13 +281,22 @@ CBGPU_API int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx
                                     int32_t* split_bin, int32_t* n_splits, double* leaf_values, void* leaf_of,
                                     int32_t leaf_of_bytes);
 
+/* Loss parameters of the grouped families; NULL takes the defaults. */
+typedef struct {
+    double l2_leaf_reg;     /* the unscaled l2 of PairLogitPairwise's scorer and leaves
+                               (boosting.rs:8270-8300); < 0: use args->scaled_l2 */
+    double softmax_lambda;  /* QuerySoftMax lambda (runtime.rs:541, default 0.01) */
+    double softmax_beta;    /* QuerySoftMax beta (runtime.rs:545, default 1.0) */
+} cbgpu_rank_params;
+
 /* The seam's grouped families (FamilyTreeArgs::Ranking / ::Pairwise,
- * runtime.rs:918-934) for QueryRMSE, PairLogit and PairLogitPairwise: the
- * reference's device session declines them
+ * runtime.rs:918-934) for QueryRMSE, QuerySoftMax, PairLogit and
+ * PairLogitPairwise: the reference's device session declines them
  * (crates/cb-backend/src/gpu_runtime/session.rs:1401-1444); this mode
  * reproduces cb-train's grouped CPU branch (grouped ders,
  * crates/cb-compute/src/ranking_der.rs:139-440; PairLogit's pairwise
- * histogram weights, boosting.rs:1761-1780; Newton leaves) on one GPU.
+ * histogram weights, boosting.rs:1761-1780; Newton leaves, Gradient leaves for
+ * QuerySoftMax, boosting.rs:8330-8400) on one GPU.
  * PairLogitPairwise scores splits with the pairwise scorer
  * (crates/cb-compute/src/pairwise_scoring.rs:101-580) and takes Cholesky
  * pairwise leaves (crates/cb-train/src/pairwise_leaves.rs:51-242), both with
@@ -294,8 +304,7 @@ CBGPU_API int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx
  *  group_offsets [n_groups + 1] contiguous groups over object order, 0..n;
  *  pair_winner / pair_loser [n_pairs] global object ids of the pairs
  *                (weight 1, both in one group), ignored for QueryRMSE;
- *  l2_leaf_reg   the unscaled l2 (PairLogitPairwise only; the pointwise
- *                losses use args->scaled_l2).
+ *  params        cbgpu_rank_params or NULL (defaults).
  * The session is grown with cbgpu_multi_grow_tree at approx_dim 1 (target =
  * the relevance per object); its leaf_values are the raw deltas, and the
  * resident approximant advances by the pair-loss-centred deltas x lr, as
@@ -303,7 +312,7 @@ CBGPU_API int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx
  * random_strength and more than one GPU. */
 CBGPU_API int cbgpu_rank_begin_raw(const cbgpu_begin_args* args, const int64_t* group_offsets, int32_t n_groups,
                                    const int64_t* pair_winner, const int64_t* pair_loser, int64_t n_pairs,
-                                   double l2_leaf_reg, const float* const* float_columns, const double* borders_flat,
+                                   const cbgpu_rank_params* params, const float* const* float_columns, const double* borders_flat,
                                    const int32_t* border_counts, cbgpu_multi_session** out);
 
 /* The resident approximant, DIM-major [K * n] (flushes the pending update).

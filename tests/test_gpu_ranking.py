@@ -1,4 +1,4 @@
-"""The grouped-loss (QueryRMSE, PairLogit, PairLogitPairwise) device mode against upstream and the oracle.
+"""The grouped-loss (QueryRMSE, QuerySoftMax, PairLogit, PairLogitPairwise) device mode against upstream and the oracle.
 
 The device mode (csrc/multi.cu, cbgpu_rank_begin_raw) reproduces cb-train's
 grouped CPU branch: grouped ders (crates/cb-compute/src/ranking_der.rs),
@@ -33,14 +33,15 @@ def cb():
     return cb
 
 
-@pytest.mark.parametrize("loss", ["QueryRMSE", "PairLogit", "PairLogitPairwise"])
+@pytest.mark.parametrize("loss", ["QueryRMSE", "PairLogit", "PairLogitPairwise", "QuerySoftMax"])
 def test_ranking_fixture(cb, loss):
     z = np.load(GOLDEN)
     p = json.loads(str(z[f"{loss}__params"]))
     X = z["X"]
     borders = [oracle.select_borders(X[:, f], 254, "GreedyLogSum", "Min") for f in range(X.shape[1])]
     fp = cb.FitParams(loss=loss, depth=p["depth"], iterations=p["iterations"], learning_rate=p["learning_rate"],
-                      l2_leaf_reg=p["l2_leaf_reg"], random_seed=p["random_seed"], boost_from_average=False)
+                      l2_leaf_reg=p["l2_leaf_reg"], random_seed=p["random_seed"], boost_from_average=False,
+                      softmax_lambda=p.get("softmax_lambda", 0.01), softmax_beta=p.get("softmax_beta", 1.0))
     m = cb.fit_ranking([X[:, f].copy() for f in range(X.shape[1])], borders, z["y"], z["group_offsets"], fp,
                        pairs=z["pairs"], staged=True)
     np.testing.assert_array_equal(m.split_feature, z[f"{loss}__split_feature"])
@@ -73,7 +74,7 @@ def _ranking_data(n_groups, F, seed):
 
 
 @pytest.mark.parametrize("loss,depth,score", [("QueryRMSE", 6, "Cosine"), ("PairLogit", 5, "Cosine"),
-                                              ("PairLogit", 4, "L2")])
+                                              ("PairLogit", 4, "L2"), ("QuerySoftMax", 6, "Cosine")])
 def test_ranking_matches_oracle(cb, loss, depth, score):
     X, y, offsets, pairs = _ranking_data(300, 10, 7 + depth)
     F = X.shape[1]
@@ -87,6 +88,26 @@ def test_ranking_matches_oracle(cb, loss, depth, score):
     np.testing.assert_array_equal(m.split_feature, o.split_feature)
     np.testing.assert_array_equal(m.split_bin, o.split_bin)
     assert np.max(np.abs(m.raw_leaf_values - o.raw_leaf_values)) <= TOL
+    assert np.max(np.abs(m.leaf_values - o.leaf_values)) <= TOL
+    assert np.max(np.abs(m.staged - o.staged)) <= TOL
+
+
+@pytest.mark.parametrize("loss,lam,beta", [("QueryRMSE", 0.01, 1.0), ("QuerySoftMax", 0.01, 1.0),
+                                           ("QuerySoftMax", 0.1, 2.0)])
+def test_weighted_ranking_matches_oracle(cb, loss, lam, beta):
+    # object weights with zeros: QuerySoftMax skips w <= 0 objects in its max, sums and ders
+    X, y, offsets, pairs = _ranking_data(150, 8, 23)
+    n, F = X.shape
+    w = np.random.RandomState(5).choice([0.0, 0.5, 1.0, 2.0], size=n)
+    borders = [oracle.select_borders(X[:, f], 48) for f in range(F)]
+    fp = cb.FitParams(loss=loss, depth=5, iterations=4, learning_rate=0.2, l2_leaf_reg=2.0,
+                      boost_from_average=False, softmax_lambda=lam, softmax_beta=beta)
+    m = cb.fit_ranking([X[:, f].copy() for f in range(F)], borders, y, offsets, fp, weights=w, staged=True)
+    bins = oracle.quantize(X.T.copy(), borders)
+    o = oracle.train_ranking(bins, [len(b) for b in borders], y, offsets, loss=loss, depth=5, iterations=4,
+                             learning_rate=0.2, l2_leaf_reg=2.0, weights=w, softmax_lambda=lam, softmax_beta=beta)
+    np.testing.assert_array_equal(m.split_feature, o.split_feature)
+    np.testing.assert_array_equal(m.split_bin, o.split_bin)
     assert np.max(np.abs(m.leaf_values - o.leaf_values)) <= TOL
     assert np.max(np.abs(m.staged - o.staged)) <= TOL
 
