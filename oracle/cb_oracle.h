@@ -187,7 +187,8 @@ void orc_solve_symmetric_newton(const double* sum_der, const double* sum_der2_pa
                                 double scaled_l2, double* out);
 
 /* ---- grouped (ranking) losses, pointwise histograms -------------------- */
-enum { ORC_RANK_QUERYRMSE = 0, ORC_RANK_PAIRLOGIT = 1, ORC_RANK_PAIRLOGIT_PAIRWISE = 2, ORC_RANK_QUERYSOFTMAX = 3 };
+enum { ORC_RANK_QUERYRMSE = 0, ORC_RANK_PAIRLOGIT = 1, ORC_RANK_PAIRLOGIT_PAIRWISE = 2, ORC_RANK_QUERYSOFTMAX = 3,
+       ORC_RANK_LAMBDAMART = 4 };
 
 /* The greedy oblivious search of the scalar loop, exported for the grouped
  * loop: returns the splits taken; leaf_of gets the final leaf ids. */
@@ -216,6 +217,9 @@ typedef struct {
     uint64_t random_seed;
     double softmax_lambda;         /* QuerySoftMax lambda (default 0.01) */
     double softmax_beta;           /* QuerySoftMax beta (default 1.0) */
+    double lambdamart_sigma;       /* LambdaMart sigma (default 1.0) */
+    int64_t lambdamart_top;        /* LambdaMart top (-1: the whole group) */
+    int32_t lambdamart_norm;       /* LambdaMart norm (default 1) */
 } orc_rank_args;
 
 typedef struct {

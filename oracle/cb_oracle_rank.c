@@ -1,7 +1,8 @@
 /*
  * cb_oracle_rank.c -- CPU restatement of catboost_rs's grouped (ranking)
- * losses on the oblivious loop: QueryRMSE, QuerySoftMax and PairLogit on
- * pointwise histograms, and PairLogitPairwise with the pairwise split scoring and
+ * losses on the oblivious loop: QueryRMSE, QuerySoftMax, LambdaMart (NDCG /
+ * DCG) and PairLogit on pointwise histograms, and PairLogitPairwise with the
+ * pairwise split scoring and
  * Cholesky leaves (crates/cb-compute/src/ranking_der.rs, pairwise_scoring.rs,
  * crates/cb-train/src/boosting.rs grouped branch, pairwise_leaves.rs,
  * tree.rs:3740-3960, query_info.rs).
@@ -18,7 +19,13 @@
  *     takes p = e^(beta (a - max)) w / sum over the group (max over w > 0),
  *     der1 = beta (-sumWT p + w t), der2 = beta sumWT (beta p (p - 1) - lambda)
  *     with sumWT = sum(w t) over w > 0, t > 0 (ders 0 when sumWT <= 0 or
- *     w <= 0);  the ders already carry the weights;
+ *     w <= 0); LambdaMart (ranking_der.rs:440-630, loss.rs:660-680) stable-sorts
+ *     the group by approx descending and scatters each ordered pair's lambda
+ *     (first target > second target; the second position bounded by top)
+ *     with delta = (t1 - t2) |1/log2(2 + p1) - 1/log2(2 + p2)| / idealDCG,
+ *     / (0.01 + |a1 - a2|) under norm, then rescales the group by
+ *     log2(1 + sumDer1) / sumDer1 under norm;  the ders already carry the
+ *     weights;
  *  2. the histogram weight channel: PairLogit uses the pairwise weights
  *     (calc_pairwise_weights, boosting.rs:1761-1780), QueryRMSE the object
  *     weights;
@@ -73,6 +80,75 @@ static int build_competitors(const orc_rank_args* a, competitors* c) {
     for (int64_t k = 0; k < a->n_pairs; ++k) c->loser[fill[a->pair_winner[k]]++] = a->pair_loser[k];
     free(fill);
     return 0;
+}
+
+/* ndcg_denominator (ranking_der.rs:456-467): log2(2 + pos) as log(x) * log2(e) */
+static double lm_den(int64_t pos) { return log(2.0 + (double)pos) * 1.4426950408889634; }
+
+/* LambdaMart ders of one group (lambdamart_group_der, ranking_der.rs:482-606;
+ * lambdamart_pair_grad, loss.rs:673-679), NDCG / DCG; order and ts are
+ * group-sized scratch. */
+static void lambdamart_group(const double* ap, const double* tg, int64_t cnt, double sigma, int64_t top, int norm,
+                             int64_t* order, double* ts, double* d1, double* d2) {
+    for (int64_t i = 0; i < cnt; ++i) {
+        d1[i] = 0.0;
+        d2[i] = 0.0;
+    }
+    if (cnt <= 1) return;
+    for (int64_t i = 0; i < cnt; ++i) order[i] = i;
+    for (int64_t i = 1; i < cnt; ++i) { /* stable insertion sort, approx descending */
+        const int64_t key = order[i];
+        int64_t j = i - 1;
+        while (j >= 0 && ap[order[j]] < ap[key]) {
+            order[j + 1] = order[j];
+            --j;
+        }
+        order[j + 1] = key;
+    }
+    const int same = fabs(ap[order[0]] - ap[order[cnt - 1]]) == 0.0;
+    const int64_t top_size = (top == -1 || top > cnt) ? cnt : top;
+    /* lambdamart_ideal_ndcg (ranking_der.rs:616-628) */
+    for (int64_t i = 0; i < cnt; ++i) ts[i] = tg[i];
+    for (int64_t i = 1; i < cnt; ++i) {
+        const double key = ts[i];
+        int64_t j = i - 1;
+        while (j >= 0 && ts[j] < key) {
+            ts[j + 1] = ts[j];
+            --j;
+        }
+        ts[j + 1] = key;
+    }
+    double ideal = 0.0;
+    for (int64_t p = 0; p < top_size; ++p) ideal += ts[p] / lm_den(p);
+    double sum_der1 = 0.0;
+    for (int64_t fi = 0; fi < cnt; ++fi) {
+        const int64_t bound = fi < top_size ? cnt : top_size;
+        for (int64_t si = 0; si < bound; ++si) {
+            const double ft = tg[order[fi]], st = tg[order[si]];
+            if (ft <= st) continue;
+            const double adiff = ap[order[fi]] - ap[order[si]];
+            const double dnum = ft - st;
+            const double dden = fabs(1.0 / lm_den(fi) - 1.0 / lm_den(si));
+            double delta = ideal != 0.0 ? dnum * dden / ideal : 0.0;
+            if (norm && !same) delta /= 0.01 + fabs(adiff);
+            const double sig = 1.0 / (1.0 + exp(sigma * adiff));
+            double hess = sig * (1.0 - sig);
+            const double anti = -sigma * delta * sig;
+            hess *= sigma * sigma * delta;
+            d1[order[fi]] += anti;
+            d2[order[fi]] += hess;
+            d1[order[si]] -= anti;
+            d2[order[si]] += hess;
+            sum_der1 -= 2.0 * anti;
+        }
+    }
+    if (norm && sum_der1 > 0.0) {
+        const double norma = log2(1.0 + sum_der1) / sum_der1;
+        for (int64_t i = 0; i < cnt; ++i) {
+            d1[i] *= norma;
+            d2[i] *= norma;
+        }
+    }
 }
 
 /* ---- pairwise scoring (crates/cb-compute/src/pairwise_scoring.rs) ------- */
@@ -288,6 +364,7 @@ int orc_train_ranking(const orc_rank_args* a, orc_rank_out* o) {
     double* sh = (double*)malloc(sizeof(double) * ((size_t)n + 1));
     double* tmp = (double*)malloc(sizeof(double) * ((size_t)(n > L ? n : L) + 1));
     int32_t* leaf = (int32_t*)malloc(sizeof(int32_t) * ((size_t)n + 1));
+    int64_t* lm_order = (int64_t*)malloc(sizeof(int64_t) * ((size_t)n + 1));
     double* lv = (double*)malloc(sizeof(double) * L);
     double* lw = (double*)malloc(sizeof(double) * L);
 
@@ -330,7 +407,10 @@ int orc_train_ranking(const orc_rank_args* a, orc_rank_out* o) {
         for (int32_t g = 0; g < a->n_groups; ++g) {
             const int64_t b = a->group_offsets[g], e = a->group_offsets[g + 1];
             if (e <= b) continue;
-            if (a->loss == ORC_RANK_QUERYSOFTMAX) {
+            if (a->loss == ORC_RANK_LAMBDAMART) {
+                lambdamart_group(approx + b, a->target + b, e - b, a->lambdamart_sigma, a->lambdamart_top,
+                                 a->lambdamart_norm, lm_order, tmp, d1 + b, d2 + b);
+            } else if (a->loss == ORC_RANK_QUERYSOFTMAX) {
                 const double beta = a->softmax_beta, lambda = a->softmax_lambda;
                 double max_a = -DBL_MAX;
                 int64_t nt = 0;
@@ -464,5 +544,6 @@ int orc_train_ranking(const orc_rank_args* a, orc_rank_out* o) {
     free(pairs_w);
     free(pairs_l);
     free(w); free(approx); free(d1); free(d2); free(eff); free(sh); free(tmp); free(leaf); free(lv); free(lw);
+    free(lm_order);
     return rc;
 }

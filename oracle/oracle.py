@@ -81,6 +81,7 @@ class _RankArgs(C.Structure):
         ("pair_loser", C.c_void_p), ("depth", C.c_int32), ("iterations", C.c_int32),
         ("learning_rate", C.c_double), ("l2_leaf_reg", C.c_double), ("score_function", C.c_int32),
         ("random_seed", C.c_uint64), ("softmax_lambda", C.c_double), ("softmax_beta", C.c_double),
+        ("lambdamart_sigma", C.c_double), ("lambdamart_top", C.c_int64), ("lambdamart_norm", C.c_int32),
     ]
 
 
@@ -89,7 +90,7 @@ class _RankOut(C.Structure):
                 ("raw_leaf_values", C.c_void_p), ("staged", C.c_void_p)]
 
 
-RANK_LOSS = {"QueryRMSE": 0, "PairLogit": 1, "PairLogitPairwise": 2, "QuerySoftMax": 3}
+RANK_LOSS = {"QueryRMSE": 0, "PairLogit": 1, "PairLogitPairwise": 2, "QuerySoftMax": 3, "LambdaMart": 4}
 
 
 def lib():
@@ -400,10 +401,11 @@ class OracleRankFit:
 
 def train_ranking(bins_fm, border_counts, target, group_offsets, *, loss="QueryRMSE", pairs=None, depth=6,
                   iterations=10, learning_rate=0.1, l2_leaf_reg=3.0, score_function="Cosine", random_seed=0,
-                  weights=None, staged=True, softmax_lambda=0.01, softmax_beta=1.0) -> OracleRankFit:
+                  weights=None, staged=True, softmax_lambda=0.01, softmax_beta=1.0, lambdamart_sigma=1.0,
+                  lambdamart_top=-1, lambdamart_norm=True) -> OracleRankFit:
     """The reference's grouped-loss CPU loop: QueryRMSE / PairLogit (pointwise histograms, Newton
-    leaves), QuerySoftMax (pointwise histograms, Gradient leaves) and PairLogitPairwise (pairwise
-    scoring, Cholesky pairwise leaves)."""
+    leaves), QuerySoftMax (pointwise histograms, Gradient leaves), LambdaMart (NDCG lambdas, Newton
+    leaves) and PairLogitPairwise (pairwise scoring, Cholesky pairwise leaves)."""
     bins = np.ascontiguousarray(bins_fm, dtype=np.uint8)
     F, n = bins.shape
     bc = np.ascontiguousarray(border_counts, dtype=np.int32)
@@ -421,7 +423,7 @@ def train_ranking(bins_fm, border_counts, target, group_offsets, *, loss="QueryR
     st = np.empty((iterations, n), dtype=np.float64) if staged else None
     args = _RankArgs(n, F, _p(bins), _p(bc), _p(t), _p(w), RANK_LOSS[loss], go.size - 1, _p(go), pw.size, _p(pw),
                      _p(pl), depth, iterations, learning_rate, l2_leaf_reg, SCORE[score_function], random_seed,
-                     softmax_lambda, softmax_beta)
+                     softmax_lambda, softmax_beta, lambdamart_sigma, lambdamart_top, int(bool(lambdamart_norm)))
     out = _RankOut(_p(sf), _p(sb), _p(lv), _p(raw), _p(st))
     rc = lib().orc_train_ranking(C.byref(args), C.byref(out))
     if rc != 0:

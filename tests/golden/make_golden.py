@@ -234,7 +234,7 @@ def multiclass_fixture(ref):
 
 
 def ranking_fixtures(ref):
-    """Upstream QueryRMSE / PairLogit / PairLogitPairwise / QuerySoftMax fixtures on the reference's frozen ranking
+    """Upstream QueryRMSE / PairLogit / PairLogitPairwise / QuerySoftMax / LambdaMart fixtures on the reference's frozen ranking
     corpus (12 objects, 5 contiguous groups, 7 explicit pairs): inputs, group
     offsets, pairs, and per loss the trees, leaf values and staged approximants."""
     fx = os.path.join(ref, "crates/cb-oracle/fixtures/ranking_corpus")
@@ -244,7 +244,7 @@ def ranking_fixtures(ref):
                   y=np.load(os.path.join(fx, "inputs/y.npy")).astype(np.float64), group_offsets=offsets,
                   pairs=np.load(os.path.join(fx, "inputs/pairs.npy")).astype(np.int64))
     losses = []
-    for loss in ("QueryRMSE", "PairLogit", "PairLogitPairwise", "QuerySoftMax"):
+    for loss in ("QueryRMSE", "PairLogit", "PairLogitPairwise", "QuerySoftMax", "LambdaMart"):
         cfg = json.loads(_read(os.path.join(fx, loss, "config.json")))
         model = json.loads(_read(os.path.join(fx, loss, "model.json")))
         mparams = model["model_info"].get("params")
@@ -262,7 +262,10 @@ def ranking_fixtures(ref):
             "depth": int(cfg["depth"]), "iterations": int(cfg["iterations"]),
             "learning_rate": float(cfg["learning_rate"]), "l2_leaf_reg": l2,
             "random_seed": int(cfg["random_seed"]), "leaf_estimation_method": tlo.get("leaf_estimation_method"),
-            "softmax_lambda": float(lf.get("lambda", 0.01)), "softmax_beta": float(lf.get("beta", 1.0))}))
+            "softmax_lambda": float(lf.get("lambda", 0.01)), "softmax_beta": float(lf.get("beta", 1.0)),
+            "lambdamart_sigma": float(lf.get("sigma", 1.0)), "lambdamart_top": int(lf.get("top", -1)),
+            "lambdamart_norm": str(lf.get("norm", "true")).lower() == "true",
+            "lambdamart_metric": str(lf.get("metric", "NDCG"))}))
         losses.append(loss)
     np.savez_compressed(os.path.join(OUT, "ranking_corpus.npz"), **arrays)
     return ["ranking_corpus/" + l for l in losses]

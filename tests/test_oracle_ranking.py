@@ -1,11 +1,13 @@
-"""Pin the oracle's grouped-loss loop (QueryRMSE, PairLogit, PairLogitPairwise, QuerySoftMax) to upstream.
+"""Pin the oracle's grouped-loss loop (QueryRMSE, PairLogit, PairLogitPairwise, QuerySoftMax, LambdaMart) to upstream.
 
 tests/golden/ranking_corpus.npz comes from the reference's frozen ranking
 corpus (crates/cb-oracle/fixtures/ranking_corpus: 12 objects in 5 contiguous
 groups, 7 explicit pairs, depth 2, 5 iterations, lr 0.3), which the
 reference's own ranking oracle tests train against.  QuerySoftMax takes a
 per-group softmax der (crates/cb-compute/src/ranking_der.rs:247-320) and
-Gradient leaves (the fixture's leaf_estimation_method).  PairLogitPairwise scores
+Gradient leaves (the fixture's leaf_estimation_method); LambdaMart the NDCG
+lambda ders of a stable approx-descending sort (ranking_der.rs:482-628) with
+Newton leaves.  PairLogitPairwise scores
 splits with the pairwise statistics and a per-candidate Cholesky solve
 (crates/cb-compute/src/pairwise_scoring.rs) and takes its leaves from the
 pairwise Cholesky system (crates/cb-train/src/pairwise_leaves.rs).  Trees are compared
@@ -38,11 +40,15 @@ def _fit(d, loss, borders, **kw):
     if loss == "QuerySoftMax":
         assert p["leaf_estimation_method"] == "Gradient"
         args.update(softmax_lambda=p["softmax_lambda"], softmax_beta=p["softmax_beta"])
+    if loss == "LambdaMart":
+        assert p["leaf_estimation_method"] == "Newton" and p["lambdamart_metric"] == "NDCG"
+        args.update(lambdamart_sigma=p["lambdamart_sigma"], lambdamart_top=p["lambdamart_top"],
+                    lambdamart_norm=p["lambdamart_norm"])
     args.update(kw)
     return oracle.train_ranking(bins, [len(b) for b in borders], d["y"], d["group_offsets"], **args)
 
 
-@pytest.mark.parametrize("loss", ["QueryRMSE", "PairLogit", "PairLogitPairwise", "QuerySoftMax"])
+@pytest.mark.parametrize("loss", ["QueryRMSE", "PairLogit", "PairLogitPairwise", "QuerySoftMax", "LambdaMart"])
 @pytest.mark.parametrize("border_set", ["full", "model"])
 def test_ranking_matches_upstream(loss, border_set):
     d = _load()
