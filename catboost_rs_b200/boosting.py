@@ -32,6 +32,10 @@ class FitParams:
     boost_from_average: bool = True
     softmax_lambda: float = 0.01  # QuerySoftMax:lambda
     softmax_beta: float = 1.0     # QuerySoftMax:beta
+    lambdamart_sigma: float = 1.0  # LambdaMart:sigma
+    lambdamart_top: int = -1       # LambdaMart:top (-1: the whole group)
+    lambdamart_norm: bool = True   # LambdaMart:norm
+    lambdamart_metric: str = "NDCG"
 
 
 @dataclass
@@ -234,8 +238,8 @@ def normalize_leaf_values(pairwise: bool, lr: float, leaf_weights, raw) -> np.nd
 def fit_ranking(float_columns: Sequence[np.ndarray], borders: Sequence[Sequence[float]], target, group_offsets,
                 params: FitParams, pairs=None, weights=None, *, staged: bool = False,
                 device: int = 0) -> RankingModel:
-    """QueryRMSE / QuerySoftMax / PairLogit / PairLogitPairwise fit
-    (params.loss) on raw f32 columns with fixed borders: cb-train's grouped
+    """QueryRMSE / QuerySoftMax / LambdaMart / PairLogit / PairLogitPairwise
+    fit (params.loss) on raw f32 columns with fixed borders: cb-train's grouped
     loop (pointwise histograms with Newton or, for QuerySoftMax, Gradient
     leaves; or pairwise scoring and Cholesky leaves) over the device's ranking
     arm; leaf normalisation on the host as cb-train does it."""
@@ -253,7 +257,9 @@ def fit_ranking(float_columns: Sequence[np.ndarray], borders: Sequence[Sequence[
     n_bins = max(len(b) for b in borders) + 1
     ok = rt.begin_ranking_raw(p.loss, p.depth, True, 1, p.score_function, cols, borders, w, n, F, n_bins, lr,
                               scaled_l2, cfg, group_offsets, pairs, l2_leaf_reg=p.l2_leaf_reg,
-                              softmax_lambda=p.softmax_lambda, softmax_beta=p.softmax_beta)
+                              softmax_lambda=p.softmax_lambda, softmax_beta=p.softmax_beta,
+                              lambdamart_sigma=p.lambdamart_sigma, lambdamart_top=p.lambdamart_top,
+                              lambdamart_norm=p.lambdamart_norm, lambdamart_metric=p.lambdamart_metric)
     if not ok:
         raise RuntimeError(f"device declined: {rt.decline_reason}")
     T, D = p.iterations, p.depth

@@ -486,7 +486,22 @@ __global__ void mc_apply_pending_kernel(int64_t n, int K, int L, double* __restr
 
 // ---- ranking mode (grouped losses, K = 1) ----------------------------------
 
-enum : int { kRankQueryRmse = 0, kRankPairLogit = 1, kRankPairLogitPairwise = 2, kRankQuerySoftMax = 3 };
+enum : int { kRankQueryRmse = 0, kRankPairLogit = 1, kRankPairLogitPairwise = 2, kRankQuerySoftMax = 3,
+             kRankLambdaMart = 4 };
+
+// Per-loss parameters of rk_der_kernel.  LambdaMart's position denominators
+// log2(2 + pos) (as log(x) * log2(e), ranking_der.rs:456-467) and each group's
+// ideal DCG (lambdamart_ideal_ndcg, ranking_der.rs:616-628) are computed on
+// the host once the target is known, so they round exactly as the CPU's.
+struct RkLossParams {
+    double sm_lambda, sm_beta;
+    double lm_sigma;
+    int64_t lm_top;
+    int32_t lm_norm;
+    const double* lm_den;    // [max group size]
+    const double* lm_ideal;  // [n_groups]
+    int32_t* lm_order;       // [n] group-local sort scratch
+};
 constexpr double kPairwisePrior = 0.1;  // PairwiseNonDiagReg default (oblivious_tree_options.cpp:16)
 
 // Grouped derivatives (calc_ders_for_queries, crates/cb-compute/src/
@@ -500,17 +515,79 @@ constexpr double kPairwisePrior = 0.1;  // PairwiseNonDiagReg default (oblivious
 //             sumWT = sum(w t) over w > 0 (t > 0 terms), ew = e^(beta (a - max)) w,
 //             p = ew / sum(ew), der1 = beta (-sumWT p + w t),
 //             der2 = beta sumWT (beta p (p - 1) - lambda); 0 when sumWT <= 0 or w <= 0.
+//  LambdaMart (lambdamart_group_der, ranking_der.rs:482-606; loss.rs:673-679):
+//             stable sort by approx descending, then every ordered pair with
+//             t1 > t2 (second position bounded by top) scatters the sigmoid
+//             lambda with delta = (t1 - t2) |1/den1 - 1/den2| / idealDCG
+//             (/ (0.01 + |a1 - a2|) under norm); norm rescales the group by
+//             log2(1 + sumDer1) / sumDer1.  Object weights do not enter.
 // The ders carry the weights already (boosting.rs:7453-7490).
 __global__ void rk_der_kernel(int n_groups, int mode, const int64_t* __restrict__ goff,
                               const int64_t* __restrict__ cstart, const int64_t* __restrict__ closer,
                               const double* __restrict__ approx, const double* __restrict__ target,
-                              const double* __restrict__ weight, double sm_lambda, double sm_beta,
-                              double* __restrict__ d1, double* __restrict__ d2, McState* __restrict__ ms) {
+                              const double* __restrict__ weight, RkLossParams lp, double* __restrict__ d1,
+                              double* __restrict__ d2, McState* __restrict__ ms) {
     const int g = blockIdx.x * blockDim.x + threadIdx.x;
     if (g >= n_groups) return;
     const int64_t b = goff[g], e = goff[g + 1];
+    const double sm_lambda = lp.sm_lambda, sm_beta = lp.sm_beta;
     bool finite = true;
-    if (mode == kRankQuerySoftMax) {
+    if (mode == kRankLambdaMart) {
+        const int64_t cnt = e - b;
+        for (int64_t i = b; i < e; ++i) {
+            d1[i] = 0.0;
+            d2[i] = 0.0;
+        }
+        if (cnt > 1) {
+            int32_t* ord = lp.lm_order + b;
+            const double* ap = approx + b;
+            const double* tg = target + b;
+            for (int64_t k = 0; k < cnt; ++k) ord[k] = (int32_t)k;
+            for (int64_t k = 1; k < cnt; ++k) {  // stable insertion sort, approx descending
+                const int32_t key = ord[k];
+                int64_t j = k - 1;
+                while (j >= 0 && ap[ord[j]] < ap[key]) {
+                    ord[j + 1] = ord[j];
+                    --j;
+                }
+                ord[j + 1] = key;
+            }
+            const bool same = fabs(__dsub_rn(ap[ord[0]], ap[ord[cnt - 1]])) == 0.0;
+            const int64_t top = (lp.lm_top == -1 || lp.lm_top > cnt) ? cnt : lp.lm_top;
+            const double ideal = lp.lm_ideal[g], sigma = lp.lm_sigma;
+            double sum_der1 = 0.0;
+            for (int64_t fi = 0; fi < cnt; ++fi) {
+                const int64_t bound = fi < top ? cnt : top;
+                for (int64_t si = 0; si < bound; ++si) {
+                    const double ft = tg[ord[fi]], st = tg[ord[si]];
+                    if (ft <= st) continue;
+                    const double adiff = __dsub_rn(ap[ord[fi]], ap[ord[si]]);
+                    const double dnum = __dsub_rn(ft, st);
+                    const double dden =
+                        fabs(__dsub_rn(__ddiv_rn(1.0, lp.lm_den[fi]), __ddiv_rn(1.0, lp.lm_den[si])));
+                    double delta = ideal != 0.0 ? __ddiv_rn(__dmul_rn(dnum, dden), ideal) : 0.0;
+                    if (lp.lm_norm && !same) delta = __ddiv_rn(delta, __dadd_rn(0.01, fabs(adiff)));
+                    const double sig = __ddiv_rn(1.0, __dadd_rn(1.0, exp(__dmul_rn(sigma, adiff))));
+                    const double hess = __dmul_rn(__dmul_rn(sig, __dsub_rn(1.0, sig)),
+                                                  __dmul_rn(__dmul_rn(sigma, sigma), delta));
+                    const double anti = __dmul_rn(__dmul_rn(-sigma, delta), sig);
+                    d1[b + ord[fi]] = __dadd_rn(d1[b + ord[fi]], anti);
+                    d2[b + ord[fi]] = __dadd_rn(d2[b + ord[fi]], hess);
+                    d1[b + ord[si]] = __dsub_rn(d1[b + ord[si]], anti);
+                    d2[b + ord[si]] = __dadd_rn(d2[b + ord[si]], hess);
+                    sum_der1 = __dsub_rn(sum_der1, __dmul_rn(2.0, anti));
+                }
+            }
+            if (lp.lm_norm && sum_der1 > 0.0) {
+                const double norma = __ddiv_rn(log2(__dadd_rn(1.0, sum_der1)), sum_der1);
+                for (int64_t i = b; i < e; ++i) {
+                    d1[i] = __dmul_rn(d1[i], norma);
+                    d2[i] = __dmul_rn(d2[i], norma);
+                }
+            }
+        }
+        for (int64_t i = b; i < e; ++i) finite &= isfinite(d1[i]) && isfinite(d2[i]);
+    } else if (mode == kRankQuerySoftMax) {
         double mx = -DBL_MAX, swt = 0.0;
         for (int64_t i = b; i < e; ++i) {
             const double w = weight ? weight[i] : 1.0;
@@ -1006,9 +1083,20 @@ struct cbgpu_multi_session {
     double* d_pwscratch = nullptr;
     double raw_l2 = 0.0;
     double sm_lambda = 0.01, sm_beta = 1.0;
+    // LambdaMart: sigma / top / norm, position denominators, per-group ideal
+    // DCG (filled at the first grow, when the target arrives), sort scratch
+    double lm_sigma = 1.0;
+    int64_t lm_top = -1;
+    int32_t lm_norm = 1;
+    std::vector<int64_t> h_goff;
+    double *d_lmden = nullptr, *d_lmideal = nullptr;
+    int32_t* d_lmorder = nullptr;
 
     ~cbgpu_multi_session() {
         if (st) cudaStreamSynchronize(st);
+        cudaFree(d_lmden);
+        cudaFree(d_lmideal);
+        cudaFree(d_lmorder);
         cudaFree(d_pwin);
         cudaFree(d_pstat);
         cudaFree(d_pwsum);
@@ -1230,6 +1318,7 @@ int cbgpu_rank_begin_raw(const cbgpu_begin_args* a, const int64_t* group_offsets
     else if (a->loss == CBGPU_LOSS_PAIRLOGIT) mode = kRankPairLogit;
     else if (a->loss == CBGPU_LOSS_PAIRLOGIT_PAIRWISE) mode = kRankPairLogitPairwise;
     else if (a->loss == CBGPU_LOSS_QUERYSOFTMAX) mode = kRankQuerySoftMax;
+    else if (a->loss == CBGPU_LOSS_LAMBDAMART) mode = kRankLambdaMart;
     else return mfail(CBGPU_DECLINED, "rank_begin: loss %d is not a covered grouped loss", a->loss);
     const double l2_leaf_reg = params && params->l2_leaf_reg >= 0.0 ? params->l2_leaf_reg : a->scaled_l2;
     const double sm_lambda = params ? params->softmax_lambda : 0.01;
@@ -1237,6 +1326,14 @@ int cbgpu_rank_begin_raw(const cbgpu_begin_args* a, const int64_t* group_offsets
     if (mode == kRankQuerySoftMax && !(std::isfinite(sm_lambda) && sm_lambda >= 0.0 && std::isfinite(sm_beta) &&
                                        sm_beta > 0.0))  // LossFunction validation (runtime.rs:698-715)
         return mfail(CBGPU_ERR_INVALID, "rank_begin: QuerySoftMax needs lambda >= 0 and beta > 0, finite");
+    const double lm_sigma = params ? params->lambdamart_sigma : 1.0;
+    const int64_t lm_top = params ? params->lambdamart_top : -1;
+    if (mode == kRankLambdaMart) {
+        if (params && params->lambdamart_metric != 0 && params->lambdamart_metric != 1)
+            return mfail(CBGPU_DECLINED, "rank_begin: LambdaMart covers the NDCG / DCG metrics");
+        if (!(std::isfinite(lm_sigma) && lm_sigma > 0.0) || !(lm_top == -1 || lm_top > 0))
+            return mfail(CBGPU_ERR_INVALID, "rank_begin: LambdaMart needs sigma > 0 and top > 0 or -1");
+    }
     if (a->grow_policy != CBGPU_GROW_SYMMETRIC || !a->boosting_type_is_plain || a->fold_count != 1)
         return mfail(CBGPU_DECLINED, "rank_begin: only Plain SymmetricTree with one fold");
     if (a->score_function != CBGPU_SCORE_COSINE && a->score_function != CBGPU_SCORE_L2)
@@ -1326,12 +1423,28 @@ int cbgpu_rank_begin_raw(const cbgpu_begin_args* a, const int64_t* group_offsets
         s->n_groups = n_groups;
         s->sm_lambda = sm_lambda;
         s->sm_beta = sm_beta;
+        s->lm_sigma = lm_sigma;
+        s->lm_top = lm_top;
+        s->lm_norm = params ? (params->lambdamart_norm ? 1 : 0) : 1;
+        s->h_goff.assign(group_offsets, group_offsets + n_groups + 1);
         rc = mdalloc(&s->d_goff, (size_t)n_groups + 1);
         if (!rc) rc = mdalloc(&s->d_cstart, (size_t)n + 1);
         if (!rc) rc = mdalloc(&s->d_closer, closer.size());
         if (!rc) rc = mdalloc(&s->d_eff, (size_t)n);
         if (!rc) rc = mdalloc(&s->d_der2, (size_t)n);
         if (!rc) rc = mdalloc(&s->d_tgt, (size_t)n);
+        if (!rc && mode == kRankLambdaMart) {
+            int64_t maxg = 1;
+            for (int g = 0; g < n_groups; ++g) maxg = std::max(maxg, group_offsets[g + 1] - group_offsets[g]);
+            std::vector<double> den((size_t)maxg);
+            for (int64_t p = 0; p < maxg; ++p) den[(size_t)p] = std::log(2.0 + (double)p) * 1.4426950408889634;
+            rc = mdalloc(&s->d_lmden, den.size());
+            if (!rc) rc = mdalloc(&s->d_lmideal, (size_t)n_groups);
+            if (!rc) rc = mdalloc(&s->d_lmorder, (size_t)n);
+            if (!rc && cudaMemcpy(s->d_lmden, den.data(), sizeof(double) * den.size(), cudaMemcpyHostToDevice) !=
+                           cudaSuccess)
+                rc = mfail(CBGPU_ERR_CUDA, "rank_begin: upload failed");
+        }
         if (!rc && mode == kRankPairLogitPairwise) {
             const int L = 1 << a->depth, P = L / 2;
             s->n_pairs = n_pairs;
@@ -1389,6 +1502,23 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
     MCU(cudaSetDevice(s->device));
     if (!s->target_ready && s->rank_mode >= 0) {
         if (!target) return mfail(CBGPU_ERR_INVALID, "multi_grow: the first call needs the target");
+        if (s->rank_mode == kRankLambdaMart) {
+            // lambdamart_ideal_ndcg per group: the DCG of the relevance-sorted
+            // order over the top positions, summed in position order
+            const int G = s->n_groups;
+            std::vector<double> ideal((size_t)G), ts;
+            for (int g = 0; g < G; ++g) {
+                const int64_t b = s->h_goff[(size_t)g], e = s->h_goff[(size_t)g + 1], cnt = e - b;
+                ts.assign(target + b, target + e);
+                std::stable_sort(ts.begin(), ts.end(), [](double x, double y) { return x > y; });
+                const int64_t top = (s->lm_top == -1 || s->lm_top > cnt) ? cnt : s->lm_top;
+                double acc = 0.0;
+                for (int64_t p = 0; p < top; ++p) acc += ts[(size_t)p] / (std::log(2.0 + (double)p) * 1.4426950408889634);
+                ideal[(size_t)g] = acc;
+            }
+            MCU(cudaMemcpyAsync(s->d_lmideal, ideal.data(), sizeof(double) * (size_t)G, cudaMemcpyHostToDevice, st));
+            MCU(cudaStreamSynchronize(st));
+        }
         MCU(cudaMemcpyAsync(s->d_tgt, target, sizeof(double) * n, cudaMemcpyHostToDevice, st));
         MCU(cudaStreamSynchronize(st));
         s->target_ready = true;
@@ -1440,7 +1570,9 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
             mc_apply_pending_kernel<<<g, kMcThreads, 0, st>>>(n, 1, L, s->approx, s->leaf, s->leaf_lrv);
         rk_der_kernel<<<(unsigned)((s->n_groups + 127) / 128), 128, 0, st>>>(
             s->n_groups, s->rank_mode, s->d_goff, s->d_cstart, s->d_closer, s->approx, s->d_tgt, s->weight,
-            s->sm_lambda, s->sm_beta, s->wd1, s->d_der2, s->d_ms);
+            RkLossParams{s->sm_lambda, s->sm_beta, s->lm_sigma, s->lm_top, s->lm_norm, s->d_lmden, s->d_lmideal,
+                         s->d_lmorder},
+            s->wd1, s->d_der2, s->d_ms);
     } else {
         mc_der_kernel<<<g, kMcThreads, 0, st>>>(n, K, s->approx, s->target, s->weight, s->leaf, s->leaf_lrv, L,
                                                 s->pending ? 1 : 0, s->wd1, s->d_ms);

@@ -19,7 +19,9 @@ import numpy as np
 from . import _lib
 
 LOSS = {"RMSE": 0, "Rmse": 0, "Logloss": 1, "CrossEntropy": 2, "MultiClass": 3, "QueryRMSE": 4, "PairLogit": 5,
-        "PairLogitPairwise": 6, "QuerySoftMax": 7}
+        "PairLogitPairwise": 6, "QuerySoftMax": 7,
+        "LambdaMart": 8}
+LAMBDAMART_METRIC = {"NDCG": 0, "DCG": 1, "MRR": 2, "ERR": 3, "MAP": 4}
 SCORE = {"Cosine": 0, "L2": 1, "SolarL2": 2, "NewtonL2": 3, "NewtonCosine": 4, "LOOL2": 5, "SatL2": 6}
 BOOT = {"No": 0, "Bayesian": 1, "Bernoulli": 2, "MVS": 3, "Mvs": 3, "Poisson": 4}
 GROW = {"SymmetricTree": 0, "Depthwise": 1, "Lossguide": 2, "Region": 3}
@@ -318,12 +320,14 @@ class B200MultiRuntime(B200Runtime):
     def begin_ranking_raw(self, loss, depth, boosting_type_is_plain, fold_count, score_function, float_columns,
                           feature_borders, weight, n, n_features, n_bins, learning_rate, scaled_l2,
                           config: DeviceTrainConfig, group_offsets, pairs=None, l2_leaf_reg=None,
-                          softmax_lambda=0.01, softmax_beta=1.0) -> bool:
+                          softmax_lambda=0.01, softmax_beta=1.0, lambdamart_sigma=1.0, lambdamart_top=-1,
+                          lambdamart_norm=True, lambdamart_metric="NDCG") -> bool:
         """The grouped families (FamilyTreeArgs::Ranking / ::Pairwise) for
-        QueryRMSE / QuerySoftMax / PairLogit / PairLogitPairwise: group offsets
+        QueryRMSE / QuerySoftMax / LambdaMart / PairLogit / PairLogitPairwise: group offsets
         [n_groups + 1] and, for the pair losses, (winner, loser) global object
         ids; l2_leaf_reg is the unscaled l2 the pairwise scorer and leaves use
-        (default scaled_l2); QuerySoftMax's lambda and beta; grown with
+        (default scaled_l2); QuerySoftMax's lambda and beta; LambdaMart's
+        sigma, top, norm and metric (NDCG / DCG); grown with
         grow_tree_on_device (family None, approx_dim 1)."""
         self.end_device_training()
         cols = [np.ascontiguousarray(c, dtype=np.float32) for c in float_columns]
@@ -342,7 +346,8 @@ class B200MultiRuntime(B200Runtime):
                        n_features, n_bins, learning_rate, scaled_l2, config)
         self._keep += [go, pw, pl]
         rp = _lib.RankParams(-1.0 if l2_leaf_reg is None else float(l2_leaf_reg), float(softmax_lambda),
-                             float(softmax_beta))
+                             float(softmax_beta), float(lambdamart_sigma), int(lambdamart_top),
+                             1 if lambdamart_norm else 0, LAMBDAMART_METRIC[lambdamart_metric])
         rc = self._L.cbgpu_rank_begin_raw(C.byref(a), _ptr(go), go.size - 1, _ptr(pw), _ptr(pl), pw.size,
                                           C.byref(rp), colptrs, _ptr(flat), _ptr(counts), C.byref(self._s))
         ok = self._finish_begin(rc, n, depth)

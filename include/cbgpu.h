@@ -51,7 +51,7 @@ typedef enum {
 typedef enum {
     CBGPU_LOSS_RMSE = 0, CBGPU_LOSS_LOGLOSS = 1, CBGPU_LOSS_CROSSENTROPY = 2, CBGPU_LOSS_MULTICLASS = 3,
     CBGPU_LOSS_QUERYRMSE = 4, CBGPU_LOSS_PAIRLOGIT = 5, CBGPU_LOSS_PAIRLOGIT_PAIRWISE = 6,
-    CBGPU_LOSS_QUERYSOFTMAX = 7
+    CBGPU_LOSS_QUERYSOFTMAX = 7, CBGPU_LOSS_LAMBDAMART = 8
 } cbgpu_loss;
 
 /* EScoreFunction (runtime.rs:834-864); Cosine is the default. */
@@ -287,10 +287,14 @@ typedef struct {
                                (boosting.rs:8270-8300); < 0: use args->scaled_l2 */
     double softmax_lambda;  /* QuerySoftMax lambda (runtime.rs:541, default 0.01) */
     double softmax_beta;    /* QuerySoftMax beta (runtime.rs:545, default 1.0) */
+    double lambdamart_sigma;   /* LambdaMart sigma (runtime.rs:374-388, default 1.0) */
+    int64_t lambdamart_top;    /* LambdaMart top; -1 = the whole group (default) */
+    int32_t lambdamart_norm;   /* LambdaMart norm (default 1) */
+    int32_t lambdamart_metric; /* 0 = NDCG (default), 1 = DCG; MRR / ERR / MAP decline */
 } cbgpu_rank_params;
 
 /* The seam's grouped families (FamilyTreeArgs::Ranking / ::Pairwise,
- * runtime.rs:918-934) for QueryRMSE, QuerySoftMax, PairLogit and
+ * runtime.rs:918-934) for QueryRMSE, QuerySoftMax, LambdaMart, PairLogit and
  * PairLogitPairwise: the reference's device session declines them
  * (crates/cb-backend/src/gpu_runtime/session.rs:1401-1444); this mode
  * reproduces cb-train's grouped CPU branch (grouped ders,

@@ -1,4 +1,5 @@
-"""The grouped-loss (QueryRMSE, QuerySoftMax, PairLogit, PairLogitPairwise) device mode against upstream and the oracle.
+"""The grouped-loss (QueryRMSE, QuerySoftMax, LambdaMart, PairLogit, PairLogitPairwise) device mode against upstream
+and the oracle.
 
 The device mode (csrc/multi.cu, cbgpu_rank_begin_raw) reproduces cb-train's
 grouped CPU branch: grouped ders (crates/cb-compute/src/ranking_der.rs),
@@ -33,7 +34,7 @@ def cb():
     return cb
 
 
-@pytest.mark.parametrize("loss", ["QueryRMSE", "PairLogit", "PairLogitPairwise", "QuerySoftMax"])
+@pytest.mark.parametrize("loss", ["QueryRMSE", "PairLogit", "PairLogitPairwise", "QuerySoftMax", "LambdaMart"])
 def test_ranking_fixture(cb, loss):
     z = np.load(GOLDEN)
     p = json.loads(str(z[f"{loss}__params"]))
@@ -41,7 +42,9 @@ def test_ranking_fixture(cb, loss):
     borders = [oracle.select_borders(X[:, f], 254, "GreedyLogSum", "Min") for f in range(X.shape[1])]
     fp = cb.FitParams(loss=loss, depth=p["depth"], iterations=p["iterations"], learning_rate=p["learning_rate"],
                       l2_leaf_reg=p["l2_leaf_reg"], random_seed=p["random_seed"], boost_from_average=False,
-                      softmax_lambda=p.get("softmax_lambda", 0.01), softmax_beta=p.get("softmax_beta", 1.0))
+                      softmax_lambda=p.get("softmax_lambda", 0.01), softmax_beta=p.get("softmax_beta", 1.0),
+                      lambdamart_sigma=p.get("lambdamart_sigma", 1.0), lambdamart_top=p.get("lambdamart_top", -1),
+                      lambdamart_norm=p.get("lambdamart_norm", True))
     m = cb.fit_ranking([X[:, f].copy() for f in range(X.shape[1])], borders, z["y"], z["group_offsets"], fp,
                        pairs=z["pairs"], staged=True)
     np.testing.assert_array_equal(m.split_feature, z[f"{loss}__split_feature"])
@@ -112,6 +115,25 @@ def test_weighted_ranking_matches_oracle(cb, loss, lam, beta):
     assert np.max(np.abs(m.staged - o.staged)) <= TOL
 
 
+@pytest.mark.parametrize("top,norm,sigma", [(-1, True, 1.0), (5, True, 2.0), (-1, False, 0.5), (300, True, 1.0)])
+def test_lambdamart_matches_oracle(cb, top, norm, sigma):
+    # groups of 20-120 documents: the per-group sort, the top cut and the norm rescale
+    X, y, offsets, pairs = _ranking_data(120, 8, 31)
+    n, F = X.shape
+    borders = [oracle.select_borders(X[:, f], 48) for f in range(F)]
+    fp = cb.FitParams(loss="LambdaMart", depth=5, iterations=4, learning_rate=0.2, l2_leaf_reg=3.0,
+                      boost_from_average=False, lambdamart_sigma=sigma, lambdamart_top=top, lambdamart_norm=norm)
+    m = cb.fit_ranking([X[:, f].copy() for f in range(F)], borders, y, offsets, fp, staged=True)
+    bins = oracle.quantize(X.T.copy(), borders)
+    o = oracle.train_ranking(bins, [len(b) for b in borders], y, offsets, loss="LambdaMart", depth=5, iterations=4,
+                             learning_rate=0.2, l2_leaf_reg=3.0, lambdamart_sigma=sigma, lambdamart_top=top,
+                             lambdamart_norm=norm)
+    np.testing.assert_array_equal(m.split_feature, o.split_feature)
+    np.testing.assert_array_equal(m.split_bin, o.split_bin)
+    assert np.max(np.abs(m.leaf_values - o.leaf_values)) <= TOL
+    assert np.max(np.abs(m.staged - o.staged)) <= TOL
+
+
 # depth 3 and 6 keep every level's pair-weight system in shared memory (2P <= 64);
 # depth 7 scores its last level from the global scratch slots
 @pytest.mark.parametrize("depth,n_groups", [(3, 60), (6, 120), (7, 40)])
@@ -154,6 +176,13 @@ def test_ranking_declines_and_errors(cb):
     ok = rt.begin_ranking_raw("PairLogitPairwise", 9, True, 1, "Cosine", cols, borders, None, n, F, nb, 0.3, 3.0,
                               cb.DeviceTrainConfig(), offsets, pairs, l2_leaf_reg=3.0)
     assert not ok and "depth" in rt.decline_reason
+    rt = cb.B200MultiRuntime()  # LambdaMart covers NDCG / DCG only
+    ok = rt.begin_ranking_raw("LambdaMart", 3, True, 1, "Cosine", cols, borders, None, n, F, nb, 0.3, 3.0,
+                              cb.DeviceTrainConfig(), offsets, None, lambdamart_metric="MRR")
+    assert not ok and "NDCG" in rt.decline_reason
+    with pytest.raises(CbGpuError, match="sigma"):
+        cb.B200MultiRuntime().begin_ranking_raw("LambdaMart", 3, True, 1, "Cosine", cols, borders, None, n, F, nb,
+                                                0.3, 3.0, cb.DeviceTrainConfig(), offsets, None, lambdamart_sigma=0.0)
     with pytest.raises(CbGpuError, match="crosses group"):
         begin(prs=np.array([[0, int(offsets[1])]]))  # winner and loser in different groups
     with pytest.raises(CbGpuError, match="group offsets"):
