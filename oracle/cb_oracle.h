@@ -188,7 +188,7 @@ void orc_solve_symmetric_newton(const double* sum_der, const double* sum_der2_pa
 
 /* ---- grouped (ranking) losses, pointwise histograms -------------------- */
 enum { ORC_RANK_QUERYRMSE = 0, ORC_RANK_PAIRLOGIT = 1, ORC_RANK_PAIRLOGIT_PAIRWISE = 2, ORC_RANK_QUERYSOFTMAX = 3,
-       ORC_RANK_LAMBDAMART = 4 };
+       ORC_RANK_LAMBDAMART = 4, ORC_RANK_YETIRANK = 5 };
 
 /* The greedy oblivious search of the scalar loop, exported for the grouped
  * loop: returns the splits taken; leaf_of gets the final leaf ids. */
@@ -220,7 +220,21 @@ typedef struct {
     double lambdamart_sigma;       /* LambdaMart sigma (default 1.0) */
     int64_t lambdamart_top;        /* LambdaMart top (-1: the whole group) */
     int32_t lambdamart_norm;       /* LambdaMart norm (default 1) */
+    int32_t yeti_permutations;     /* YetiRank permutations (default 10) */
+    double yeti_decay;             /* YetiRank decay (default 0.85) */
 } orc_rank_args;
+
+/* YetiRank's sampler for one group (sample_pairs, crates/cb-train/src/
+ * yetirank.rs:75-171): out[w * g + l] = the sampled pair weight winner w over
+ * loser l (0: no pair). */
+void orc_yeti_sample_pairs(const double* raw_approx, const double* relevs, int64_t g, double query_weight,
+                           int32_t permutations, double decay, uint64_t query_seed, double* out);
+/* derive_query_seeds (yetirank.rs:173-184): the single-block query seeds. */
+void orc_yeti_query_seeds(uint64_t random_seed, int32_t n_groups, uint64_t* out);
+/* YetiRankTreeSeeder (yetirank.rs:262-430): for each of `trees` trees the
+ * recalc seeds (deriv, learning fold, leaf values) -> out[3 * tree + k]. */
+void orc_yeti_recalc_seeds(uint64_t random_seed, int32_t n_groups, int32_t n_features, int32_t depth, int32_t trees,
+                           uint64_t* out);
 
 typedef struct {
     int32_t* split_feature;  /* [iterations * depth] */

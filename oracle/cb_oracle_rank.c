@@ -1,8 +1,8 @@
 /*
  * cb_oracle_rank.c -- CPU restatement of catboost_rs's grouped (ranking)
  * losses on the oblivious loop: QueryRMSE, QuerySoftMax, LambdaMart (NDCG /
- * DCG) and PairLogit on pointwise histograms, and PairLogitPairwise with the
- * pairwise split scoring and
+ * DCG), PairLogit and YetiRank on pointwise histograms, and PairLogitPairwise
+ * with the pairwise split scoring and
  * Cholesky leaves (crates/cb-compute/src/ranking_der.rs, pairwise_scoring.rs,
  * crates/cb-train/src/boosting.rs grouped branch, pairwise_leaves.rs,
  * tree.rs:3740-3960, query_info.rs).
@@ -149,6 +149,244 @@ static void lambdamart_group(const double* ap, const double* tg, int64_t cnt, do
             d2[i] *= norma;
         }
     }
+}
+
+/* ---- YetiRank (crates/cb-train/src/yetirank.rs) ------------------------- */
+
+void orc_yeti_sample_pairs(const double* raw_approx, const double* relevs, int64_t g, double query_weight,
+                           int32_t permutations, double decay, uint64_t query_seed, double* out) {
+    for (int64_t k = 0; k < g * g; ++k) out[k] = 0.0;
+    if (g == 0 || permutations <= 0) return;
+    float* cw = (float*)calloc((size_t)(g * g), sizeof(float));
+    double* ea = (double*)malloc(sizeof(double) * (size_t)g);
+    double* boot = (double*)malloc(sizeof(double) * (size_t)g);
+    int64_t* idx = (int64_t*)malloc(sizeof(int64_t) * (size_t)g);
+    for (int64_t i = 0; i < g; ++i) ea[i] = exp(raw_approx[i]);
+    orc_rng r;
+    orc_rng_from_seed(&r, query_seed);
+    for (int32_t perm = 0; perm < permutations; ++perm) {
+        for (int64_t i = 0; i < g; ++i) {
+            idx[i] = i;
+            boot[i] = ea[i];
+        }
+        /* Gumbel noise, f32 draw and ratio (yetirank.rs:106-121) */
+        for (int64_t i = 0; i < g; ++i) {
+            const float u = (float)orc_rng_real1(&r);
+            const float ratio = u / (1.000001f - u);
+            boot[i] *= (double)ratio;
+        }
+        for (int64_t i = 1; i < g; ++i) { /* stable sort, descending */
+            const int64_t key = idx[i];
+            int64_t j = i - 1;
+            while (j >= 0 && boot[idx[j]] < boot[key]) {
+                idx[j + 1] = idx[j];
+                --j;
+            }
+            idx[j + 1] = key;
+        }
+        /* calc_weights_classic + add_weight (yetirank.rs:450-514), f32 storage */
+        double dc = 1.0;
+        for (int64_t d = 1; d < g; ++d) {
+            const int64_t first = idx[d - 1], second = idx[d];
+            const float rf = (float)relevs[first], rs = (float)relevs[second];
+            const float pw = (float)(0.15 * dc * (double)fabsf(rf - rs));
+            if (rf > rs) cw[first * g + second] += pw;
+            else if (rf < rs) cw[second * g + first] += pw;
+            dc *= decay;
+        }
+    }
+    const float qw = (float)query_weight, den = (float)permutations;
+    for (int64_t k = 0; k < g * g; ++k) {
+        const float wf = qw * cw[k] / den;
+        out[k] = (double)wf;
+    }
+    free(cw);
+    free(ea);
+    free(boot);
+    free(idx);
+}
+
+static uint64_t first_gen(uint64_t seed) {
+    orc_rng t;
+    orc_rng_from_seed(&t, seed);
+    return orc_rng_gen(&t);
+}
+
+void orc_yeti_query_seeds(uint64_t random_seed, int32_t n_groups, uint64_t* out) {
+    orc_rng b;
+    orc_rng_from_seed(&b, first_gen(random_seed));
+    for (int32_t g = 0; g < n_groups; ++g) out[g] = orc_rng_gen(&b);
+}
+
+/* derive_per_tree_query_seeds (yetirank.rs:215-221) */
+static void per_tree_query_seeds(uint64_t recalc, int32_t n_groups, uint64_t* out) {
+    orc_rng t;
+    orc_rng_from_seed(&t, recalc);
+    for (int32_t g = 0; g < n_groups; ++g) out[g] = first_gen(orc_rng_gen(&t));
+}
+
+/* YetiRankTreeSeeder::next_tree (yetirank.rs:340-430) */
+static void yeti_next_tree(orc_rng* r, int32_t G, int32_t F, int32_t depth, uint64_t* deriv, uint64_t* learnfold,
+                           uint64_t* leafval, uint64_t* recalc) {
+    (void)orc_rng_gen(r); /* structure-fold selection */
+    const uint64_t drs = first_gen(orc_rng_gen(r));
+    for (int32_t level = 0; level < depth; ++level) {
+        for (int32_t f = 0; f < F; ++f) (void)orc_rng_real1(r);
+        (void)orc_rng_gen(r);
+        for (int32_t f = 0; f < F; ++f) (void)orc_std_normal(r);
+    }
+    const uint64_t lrs = first_gen(first_gen(orc_rng_gen(r)));
+    const uint64_t vb = orc_rng_gen(r);
+    if (deriv) per_tree_query_seeds(drs, G, deriv);
+    if (learnfold) per_tree_query_seeds(lrs, G, learnfold);
+    if (leafval) per_tree_query_seeds(vb, G, leafval);
+    if (recalc) {
+        recalc[0] = drs;
+        recalc[1] = lrs;
+        recalc[2] = vb;
+    }
+}
+
+void orc_yeti_recalc_seeds(uint64_t random_seed, int32_t n_groups, int32_t n_features, int32_t depth, int32_t trees,
+                           uint64_t* out) {
+    orc_rng r;
+    orc_rng_from_seed(&r, random_seed);
+    for (int32_t t = 0; t < trees; ++t) yeti_next_tree(&r, n_groups, n_features, depth, NULL, NULL, NULL, out + 3 * t);
+}
+
+/* One YetiRank phase's ders: per group the sampled pairs from `ap` with the
+ * phase's query seeds, then the PairLogit der over them (pairlogit_group_der,
+ * ranking_der.rs:400-440) and, when eff != NULL, the pairwise weights
+ * (calc_pairwise_weights, boosting.rs:1761-1780), winner-ascending,
+ * loser-ascending. */
+static void yeti_phase_ders(const orc_rank_args* a, const double* ap, const double* gw, const uint64_t* seeds,
+                            double* cwbuf, double* d1, double* d2, double* eff) {
+    const int64_t n = a->n;
+    for (int64_t i = 0; i < n; ++i) {
+        d1[i] = 0.0;
+        d2[i] = 0.0;
+        if (eff) eff[i] = 0.0;
+    }
+    for (int32_t gi = 0; gi < a->n_groups; ++gi) {
+        const int64_t b = a->group_offsets[gi], e = a->group_offsets[gi + 1], g = e - b;
+        orc_yeti_sample_pairs(ap + b, a->target + b, g, gw[gi], a->yeti_permutations, a->yeti_decay, seeds[gi],
+                              cwbuf);
+        for (int64_t wl = 0; wl < g; ++wl) {
+            double wd = 0.0, wd2 = 0.0;
+            for (int64_t ll = 0; ll < g; ++ll) {
+                const double cw = cwbuf[wl * g + ll];
+                if (cw == 0.0) continue;
+                const double p = pair_prob(ap[b + wl], ap[b + ll]);
+                wd += cw * p;
+                wd2 += cw * p * (p - 1.0);
+                d1[b + ll] -= cw * p;
+                d2[b + ll] += cw * p * (p - 1.0);
+                if (eff) {
+                    eff[b + wl] += cw;
+                    eff[b + ll] += cw;
+                }
+            }
+            d1[b + wl] += wd;
+            d2[b + wl] += wd2;
+        }
+    }
+}
+
+/* Newton deltas over unit leaf weights (ordered per-leaf sums) */
+static void newton_unit(const double* d1, const double* d2, const int32_t* leaf, int64_t n, int32_t nl, double l2,
+                        double* out) {
+    double* sd = (double*)calloc((size_t)nl * 2, sizeof(double));
+    for (int64_t i = 0; i < n; ++i) {
+        sd[2 * leaf[i]] += d1[i];
+        sd[2 * leaf[i] + 1] += d2[i] * 1.0;
+    }
+    for (int32_t q = 0; q < nl; ++q) {
+        const double den = -sd[2 * q + 1] + l2;
+        out[q] = den == 0.0 ? 0.0 : sd[2 * q] / den;
+    }
+    free(sd);
+}
+
+/* The YetiRank loop (boosting.rs:4997-5060, 7347-7420, 8070-8200, 8787-8880):
+ * per tree the seeder's three per-group seed sets; the gradient / split ders
+ * and the histogram's pairwise weights from pairs sampled off the learning-fold
+ * approximant; the stored leaves (Newton, unit weights, pairwise centring,
+ * x lr) from pairs sampled off the model approximant; the learning-fold
+ * approximant advanced by its own resample's Newton deltas x lr. */
+static int train_yetirank(const orc_rank_args* a, orc_rank_out* o, int32_t NB) {
+    const int64_t n = a->n;
+    const int32_t F = a->n_features, D = a->depth, L = 1 << D, G = a->n_groups;
+    double* w = (double*)calloc((size_t)n + 1, sizeof(double));
+    for (int64_t i = 0; i < n; ++i) w[i] = a->weights ? a->weights[i] : 1.0;
+    const double sum_w = orc_sum_f64(w, n);
+    const double scaled_l2 = n == 0 ? a->l2_leaf_reg : a->l2_leaf_reg * (sum_w / (double)n);
+    const double lr = (double)(float)a->learning_rate;
+    int64_t maxg = 1;
+    double* gw = (double*)malloc(sizeof(double) * (size_t)(G > 0 ? G : 1));
+    for (int32_t gi = 0; gi < G; ++gi) { /* group weight: mean member weight (query_info.rs:180-187) */
+        const int64_t b = a->group_offsets[gi], e = a->group_offsets[gi + 1];
+        gw[gi] = e > b ? orc_sum_f64(w + b, e - b) / (double)(e - b) : 1.0;
+        if (e - b > maxg) maxg = e - b;
+    }
+    double* cwbuf = (double*)malloc(sizeof(double) * (size_t)(maxg * maxg));
+    double* approx = (double*)calloc((size_t)n + 1, sizeof(double));
+    double* lapprox = (double*)calloc((size_t)n + 1, sizeof(double));
+    double* d1 = (double*)malloc(sizeof(double) * ((size_t)n + 1));
+    double* d2 = (double*)malloc(sizeof(double) * ((size_t)n + 1));
+    double* eff = (double*)malloc(sizeof(double) * ((size_t)n + 1));
+    double* tmp = (double*)malloc(sizeof(double) * ((size_t)L + 1));
+    int32_t* leaf = (int32_t*)malloc(sizeof(int32_t) * ((size_t)n + 1));
+    double* lv = (double*)malloc(sizeof(double) * L);
+    double* lw = (double*)malloc(sizeof(double) * L);
+    uint64_t* seeds = (uint64_t*)malloc(sizeof(uint64_t) * 3 * (size_t)(G > 0 ? G : 1));
+    uint64_t* sd = seeds;
+    uint64_t* sl = seeds + G;
+    uint64_t* sv = seeds + 2 * G;
+    orc_rng seeder, unused;
+    orc_rng_from_seed(&seeder, a->random_seed);
+    orc_rng_from_seed(&unused, a->random_seed);
+    int rc = 0;
+    for (int32_t it = 0; it < a->iterations; ++it) {
+        yeti_next_tree(&seeder, G, F, D, sd, sl, sv, NULL);
+        /* gradient / split: the learning fold */
+        yeti_phase_ders(a, lapprox, gw, sd, cwbuf, d1, d2, eff);
+        int32_t* tf = o->split_feature + (size_t)it * D;
+        int32_t* tb = o->split_bin + (size_t)it * D;
+        int32_t err = 0;
+        const int taken = orc_search_tree(n, F, NB, D, a->score_function, a->bins_fm, a->border_counts, d1, eff,
+                                          scaled_l2, 0, &unused, tf, tb, leaf, &err);
+        if (err) {
+            rc = -3;
+            break;
+        }
+        const int32_t nl = 1 << taken;
+        /* stored leaves: the model approximant's resample */
+        yeti_phase_ders(a, approx, gw, sv, cwbuf, d1, d2, NULL);
+        for (int32_t q = 0; q < L; ++q) {
+            lv[q] = 0.0;
+            lw[q] = 0.0;
+        }
+        newton_unit(d1, d2, leaf, n, nl, scaled_l2, lv);
+        for (int64_t i = 0; i < n; ++i) lw[leaf[i]] += w[i];
+        if (o->raw_leaf_values) memcpy(o->raw_leaf_values + (size_t)it * L, lv, sizeof(double) * L);
+        const double total = orc_sum_f64(lw, nl);
+        if (fabs(total) > 1e-9) {
+            for (int32_t q = 0; q < nl; ++q) tmp[q] = lv[q] * lw[q];
+            const double avg = orc_sum_f64(tmp, nl) / total;
+            for (int32_t q = 0; q < nl; ++q) lv[q] = fabs(lw[q]) > 1e-9 ? lv[q] - avg : 0.0;
+        }
+        for (int32_t q = 0; q < nl; ++q) lv[q] *= lr;
+        memcpy(o->leaf_values + (size_t)it * L, lv, sizeof(double) * L);
+        for (int64_t i = 0; i < n; ++i) approx[i] += lv[leaf[i]];
+        /* the learning fold's own resample, Newton deltas x lr (no centring) */
+        yeti_phase_ders(a, lapprox, gw, sl, cwbuf, d1, d2, NULL);
+        newton_unit(d1, d2, leaf, n, nl, scaled_l2, lv);
+        for (int64_t i = 0; i < n; ++i) lapprox[i] += lv[leaf[i]] * lr;
+        if (o->staged) memcpy(o->staged + (size_t)it * n, approx, sizeof(double) * (size_t)n);
+    }
+    free(w); free(gw); free(cwbuf); free(approx); free(lapprox); free(d1); free(d2); free(eff); free(tmp);
+    free(leaf); free(lv); free(lw); free(seeds);
+    return rc;
 }
 
 /* ---- pairwise scoring (crates/cb-compute/src/pairwise_scoring.rs) ------- */
@@ -344,6 +582,7 @@ int orc_train_ranking(const orc_rank_args* a, orc_rank_out* o) {
     int32_t NB = 1;
     for (int32_t f = 0; f < F; ++f)
         if (a->border_counts[f] + 1 > NB) NB = a->border_counts[f] + 1;
+    if (a->loss == ORC_RANK_YETIRANK) return train_yetirank(a, o, NB);
     competitors cp = {NULL, NULL};
     const int pairlogit = a->loss == ORC_RANK_PAIRLOGIT || a->loss == ORC_RANK_PAIRLOGIT_PAIRWISE;
     if (pairlogit && build_competitors(a, &cp) != 0) {

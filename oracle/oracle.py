@@ -82,6 +82,7 @@ class _RankArgs(C.Structure):
         ("learning_rate", C.c_double), ("l2_leaf_reg", C.c_double), ("score_function", C.c_int32),
         ("random_seed", C.c_uint64), ("softmax_lambda", C.c_double), ("softmax_beta", C.c_double),
         ("lambdamart_sigma", C.c_double), ("lambdamart_top", C.c_int64), ("lambdamart_norm", C.c_int32),
+        ("yeti_permutations", C.c_int32), ("yeti_decay", C.c_double),
     ]
 
 
@@ -90,7 +91,7 @@ class _RankOut(C.Structure):
                 ("raw_leaf_values", C.c_void_p), ("staged", C.c_void_p)]
 
 
-RANK_LOSS = {"QueryRMSE": 0, "PairLogit": 1, "PairLogitPairwise": 2, "QuerySoftMax": 3, "LambdaMart": 4}
+RANK_LOSS = {"QueryRMSE": 0, "PairLogit": 1, "PairLogitPairwise": 2, "QuerySoftMax": 3, "LambdaMart": 4, "YetiRank": 5}
 
 
 def lib():
@@ -136,6 +137,13 @@ def lib():
         L.orc_solve_symmetric_newton.argtypes = [C.c_void_p, C.c_void_p, C.c_int32, C.c_double, C.c_void_p]
         L.orc_train_ranking.argtypes = [P(_RankArgs), P(_RankOut)]
         L.orc_train_ranking.restype = C.c_int
+        L.orc_yeti_sample_pairs.argtypes = [C.c_void_p, C.c_void_p, C.c_int64, C.c_double, C.c_int32, C.c_double,
+                                            C.c_uint64, C.c_void_p]
+        L.orc_yeti_sample_pairs.restype = None
+        L.orc_yeti_query_seeds.argtypes = [C.c_uint64, C.c_int32, C.c_void_p]
+        L.orc_yeti_query_seeds.restype = None
+        L.orc_yeti_recalc_seeds.argtypes = [C.c_uint64, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_void_p]
+        L.orc_yeti_recalc_seeds.restype = None
         L.orc_train.argtypes = [P(_TrainArgs), P(_TrainOut)]
         L.orc_train.restype = C.c_int
         _lib = L
@@ -402,10 +410,12 @@ class OracleRankFit:
 def train_ranking(bins_fm, border_counts, target, group_offsets, *, loss="QueryRMSE", pairs=None, depth=6,
                   iterations=10, learning_rate=0.1, l2_leaf_reg=3.0, score_function="Cosine", random_seed=0,
                   weights=None, staged=True, softmax_lambda=0.01, softmax_beta=1.0, lambdamart_sigma=1.0,
-                  lambdamart_top=-1, lambdamart_norm=True) -> OracleRankFit:
+                  lambdamart_top=-1, lambdamart_norm=True, yeti_permutations=10,
+                  yeti_decay=0.85) -> OracleRankFit:
     """The reference's grouped-loss CPU loop: QueryRMSE / PairLogit (pointwise histograms, Newton
     leaves), QuerySoftMax (pointwise histograms, Gradient leaves), LambdaMart (NDCG lambdas, Newton
-    leaves) and PairLogitPairwise (pairwise scoring, Cholesky pairwise leaves)."""
+    leaves), YetiRank (sampled pairs, Newton leaves, two approximants) and PairLogitPairwise (pairwise
+    scoring, Cholesky pairwise leaves)."""
     bins = np.ascontiguousarray(bins_fm, dtype=np.uint8)
     F, n = bins.shape
     bc = np.ascontiguousarray(border_counts, dtype=np.int32)
@@ -423,9 +433,34 @@ def train_ranking(bins_fm, border_counts, target, group_offsets, *, loss="QueryR
     st = np.empty((iterations, n), dtype=np.float64) if staged else None
     args = _RankArgs(n, F, _p(bins), _p(bc), _p(t), _p(w), RANK_LOSS[loss], go.size - 1, _p(go), pw.size, _p(pw),
                      _p(pl), depth, iterations, learning_rate, l2_leaf_reg, SCORE[score_function], random_seed,
-                     softmax_lambda, softmax_beta, lambdamart_sigma, lambdamart_top, int(bool(lambdamart_norm)))
+                     softmax_lambda, softmax_beta, lambdamart_sigma, lambdamart_top, int(bool(lambdamart_norm)),
+                     yeti_permutations, yeti_decay)
     out = _RankOut(_p(sf), _p(sb), _p(lv), _p(raw), _p(st))
     rc = lib().orc_train_ranking(C.byref(args), C.byref(out))
     if rc != 0:
         raise RuntimeError(f"orc_train_ranking failed rc={rc}")
     return OracleRankFit(sf, sb, lv, raw, st)
+
+
+def yeti_sample_pairs(raw_approx, relevs, query_weight=1.0, permutations=10, decay=0.85, query_seed=0):
+    """YetiRank's per-group pair sampler (crates/cb-train/src/yetirank.rs:75-171): the dense
+    [g, g] matrix of sampled pair weights, winner row over loser column."""
+    a = np.ascontiguousarray(raw_approx, dtype=np.float64)
+    r = np.ascontiguousarray(relevs, dtype=np.float64)
+    out = np.zeros((a.size, a.size), dtype=np.float64)
+    lib().orc_yeti_sample_pairs(_p(a), _p(r), a.size, query_weight, permutations, decay,
+                                C.c_uint64(query_seed & (2**64 - 1)), _p(out))
+    return out
+
+
+def yeti_query_seeds(random_seed: int, n_groups: int) -> np.ndarray:
+    out = np.zeros(n_groups, dtype=np.uint64)
+    lib().orc_yeti_query_seeds(C.c_uint64(random_seed), n_groups, _p(out))
+    return out
+
+
+def yeti_recalc_seeds(random_seed: int, n_groups: int, n_features: int, depth: int, trees: int) -> np.ndarray:
+    """The per-tree (deriv, learning-fold, leaf-value) recalc seeds of YetiRankTreeSeeder."""
+    out = np.zeros((trees, 3), dtype=np.uint64)
+    lib().orc_yeti_recalc_seeds(C.c_uint64(random_seed), n_groups, n_features, depth, trees, _p(out))
+    return out

@@ -244,9 +244,10 @@ def ranking_fixtures(ref):
                   y=np.load(os.path.join(fx, "inputs/y.npy")).astype(np.float64), group_offsets=offsets,
                   pairs=np.load(os.path.join(fx, "inputs/pairs.npy")).astype(np.int64))
     losses = []
-    for loss in ("QueryRMSE", "PairLogit", "PairLogitPairwise", "QuerySoftMax", "LambdaMart"):
-        cfg = json.loads(_read(os.path.join(fx, loss, "config.json")))
-        model = json.loads(_read(os.path.join(fx, loss, "model.json")))
+    for loss in ("QueryRMSE", "PairLogit", "PairLogitPairwise", "QuerySoftMax", "LambdaMart", "YetiRank"):
+        d = {"YetiRank": "yetirank"}.get(loss, loss)
+        cfg = json.loads(_read(os.path.join(fx, d, "config.json")))
+        model = json.loads(_read(os.path.join(fx, d, "model.json")))
         mparams = model["model_info"].get("params")
         mparams = json.loads(mparams) if isinstance(mparams, str) else (mparams or {})
         tlo = mparams.get("tree_learner_options", {})
@@ -257,7 +258,7 @@ def ranking_fixtures(ref):
                                                     dtype=np.int32)
         arrays[f"{loss}__split_border"] = np.array([[s["border"] for s in t["splits"]] for t in trees])
         arrays[f"{loss}__leaf_values"] = np.array([t["leaf_values"] for t in trees], dtype=np.float64)
-        arrays[f"{loss}__staged"] = np.load(os.path.join(fx, loss, "staged.npy")).reshape(len(trees), -1)
+        arrays[f"{loss}__staged"] = np.load(os.path.join(fx, d, "staged.npy")).reshape(len(trees), -1)
         arrays[f"{loss}__params"] = np.array(json.dumps({
             "depth": int(cfg["depth"]), "iterations": int(cfg["iterations"]),
             "learning_rate": float(cfg["learning_rate"]), "l2_leaf_reg": l2,
@@ -265,8 +266,25 @@ def ranking_fixtures(ref):
             "softmax_lambda": float(lf.get("lambda", 0.01)), "softmax_beta": float(lf.get("beta", 1.0)),
             "lambdamart_sigma": float(lf.get("sigma", 1.0)), "lambdamart_top": int(lf.get("top", -1)),
             "lambdamart_norm": str(lf.get("norm", "true")).lower() == "true",
-            "lambdamart_metric": str(lf.get("metric", "NDCG"))}))
+            "lambdamart_metric": str(lf.get("metric", "NDCG")),
+            "yeti_permutations": int(lf.get("permutations", 10)), "yeti_decay": float(lf.get("decay", 0.85))}))
         losses.append(loss)
+    # YetiRank's instrumented sampler log: one 3-document group (raw approx
+    # [0.5, -0.3, 0.1], relevances [2, 0, 1], 10 permutations, decay 0.85,
+    # random_seed 0, the reference's yetirank_oracle_test.rs:213-260), and the
+    # trainer's per-tree recalc seeds (update_pairs events: deriv, learning
+    # fold, leaf values per tree)
+    ev = [json.loads(l) for l in _read(os.path.join(fx, "yetirank/yetirank_rng_groundtruth.jsonl")).splitlines()
+          if l.strip()]
+    arrays["yeti_gt_query_seed"] = np.array([e["seed"] for e in ev if e["event"] == "query_seed"], dtype=np.uint64)
+    arrays["yeti_gt_competitors"] = np.array([[e["winner"], e["loser"], e["weight"]] for e in ev
+                                              if e["event"] == "competitor"], dtype=np.float64)
+    arrays["yeti_gt_sorted_orders"] = np.array([e["order"] for e in ev if e["event"] == "sorted_order"],
+                                               dtype=np.int64)
+    tr = [json.loads(l) for l in _read(os.path.join(
+        fx, "yetirank_pairwise/yetirank_pairwise_tree_rng_groundtruth.jsonl")).splitlines() if l.strip()]
+    arrays["yeti_gt_recalc_seeds"] = np.array([e["random_seed"] for e in tr if e["event"] == "update_pairs"],
+                                              dtype=np.uint64).reshape(-1, 3)
     np.savez_compressed(os.path.join(OUT, "ranking_corpus.npz"), **arrays)
     return ["ranking_corpus/" + l for l in losses]
 

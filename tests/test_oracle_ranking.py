@@ -1,4 +1,5 @@
-"""Pin the oracle's grouped-loss loop (QueryRMSE, PairLogit, PairLogitPairwise, QuerySoftMax, LambdaMart) to upstream.
+"""Pin the oracle's grouped-loss loop (QueryRMSE, PairLogit, PairLogitPairwise, QuerySoftMax, LambdaMart, YetiRank)
+to upstream.
 
 tests/golden/ranking_corpus.npz comes from the reference's frozen ranking
 corpus (crates/cb-oracle/fixtures/ranking_corpus: 12 objects in 5 contiguous
@@ -7,7 +8,10 @@ reference's own ranking oracle tests train against.  QuerySoftMax takes a
 per-group softmax der (crates/cb-compute/src/ranking_der.rs:247-320) and
 Gradient leaves (the fixture's leaf_estimation_method); LambdaMart the NDCG
 lambda ders of a stable approx-descending sort (ranking_der.rs:482-628) with
-Newton leaves.  PairLogitPairwise scores
+Newton leaves; YetiRank pairs sampled per tree and phase from TFastRng64
+query seeds (crates/cb-train/src/yetirank.rs) with separate learning-fold and
+model approximants (boosting.rs:4997-5060, 7347-7420, 8070-8200, 8787-8880).
+PairLogitPairwise scores
 splits with the pairwise statistics and a per-candidate Cholesky solve
 (crates/cb-compute/src/pairwise_scoring.rs) and takes its leaves from the
 pairwise Cholesky system (crates/cb-train/src/pairwise_leaves.rs).  Trees are compared
@@ -40,6 +44,8 @@ def _fit(d, loss, borders, **kw):
     if loss == "QuerySoftMax":
         assert p["leaf_estimation_method"] == "Gradient"
         args.update(softmax_lambda=p["softmax_lambda"], softmax_beta=p["softmax_beta"])
+    if loss == "YetiRank":
+        args.update(yeti_permutations=p["yeti_permutations"], yeti_decay=p["yeti_decay"])
     if loss == "LambdaMart":
         assert p["leaf_estimation_method"] == "Newton" and p["lambdamart_metric"] == "NDCG"
         args.update(lambdamart_sigma=p["lambdamart_sigma"], lambdamart_top=p["lambdamart_top"],
@@ -48,7 +54,8 @@ def _fit(d, loss, borders, **kw):
     return oracle.train_ranking(bins, [len(b) for b in borders], d["y"], d["group_offsets"], **args)
 
 
-@pytest.mark.parametrize("loss", ["QueryRMSE", "PairLogit", "PairLogitPairwise", "QuerySoftMax", "LambdaMart"])
+@pytest.mark.parametrize("loss", ["QueryRMSE", "PairLogit", "PairLogitPairwise", "QuerySoftMax", "LambdaMart",
+                                  "YetiRank"])
 @pytest.mark.parametrize("border_set", ["full", "model"])
 def test_ranking_matches_upstream(loss, border_set):
     d = _load()
@@ -91,3 +98,26 @@ def test_group_offsets_validated():
     with pytest.raises(RuntimeError):
         oracle.train_ranking(bins, [len(b) for b in borders], d["y"], np.array([0, 5]), loss="QueryRMSE", depth=2,
                              iterations=1)
+
+
+def test_yetirank_sampler_matches_instrumented_log():
+    # one 3-document group, raw approx [0.5, -0.3, 0.1], relevances [2, 0, 1],
+    # 10 permutations, decay 0.85, random_seed 0 (yetirank_oracle_test.rs:213-260)
+    d = _load()
+    seed = oracle.yeti_query_seeds(0, 1)
+    np.testing.assert_array_equal(seed, d["yeti_gt_query_seed"])
+    got = oracle.yeti_sample_pairs([0.5, -0.3, 0.1], [2.0, 0.0, 1.0], 1.0, 10, 0.85, int(seed[0]))
+    want = np.zeros((3, 3))
+    for w, l, wt in d["yeti_gt_competitors"]:
+        want[int(w), int(l)] = wt
+    assert np.max(np.abs(got - want)) <= TOL  # the log prints 6 decimals
+    assert np.count_nonzero(got) == len(d["yeti_gt_competitors"])
+
+
+def test_yetirank_tree_seeder_matches_trainer_log():
+    # update_pairs events per tree: the derivative, leaf-value and learning-fold
+    # recalc seeds (the seeder draws the learning fold's before the leaf values')
+    d = _load()
+    gt = d["yeti_gt_recalc_seeds"]
+    ours = oracle.yeti_recalc_seeds(20260617, 5, 4, 2, gt.shape[0])
+    np.testing.assert_array_equal(ours[:, [0, 2, 1]], gt)
