@@ -36,6 +36,8 @@ class FitParams:
     lambdamart_top: int = -1       # LambdaMart:top (-1: the whole group)
     lambdamart_norm: bool = True   # LambdaMart:norm
     lambdamart_metric: str = "NDCG"
+    yeti_permutations: int = 10    # YetiRank:permutations
+    yeti_decay: float = 0.85       # YetiRank:decay
 
 
 @dataclass
@@ -238,8 +240,9 @@ def normalize_leaf_values(pairwise: bool, lr: float, leaf_weights, raw) -> np.nd
 def fit_ranking(float_columns: Sequence[np.ndarray], borders: Sequence[Sequence[float]], target, group_offsets,
                 params: FitParams, pairs=None, weights=None, *, staged: bool = False,
                 device: int = 0) -> RankingModel:
-    """QueryRMSE / QuerySoftMax / LambdaMart / PairLogit / PairLogitPairwise
-    fit (params.loss) on raw f32 columns with fixed borders: cb-train's grouped
+    """QueryRMSE / QuerySoftMax / LambdaMart / YetiRank / PairLogit /
+    PairLogitPairwise fit (params.loss) on raw f32 columns with fixed borders:
+    cb-train's grouped
     loop (pointwise histograms with Newton or, for QuerySoftMax, Gradient
     leaves; or pairwise scoring and Cholesky leaves) over the device's ranking
     arm; leaf normalisation on the host as cb-train does it."""
@@ -259,7 +262,8 @@ def fit_ranking(float_columns: Sequence[np.ndarray], borders: Sequence[Sequence[
                               scaled_l2, cfg, group_offsets, pairs, l2_leaf_reg=p.l2_leaf_reg,
                               softmax_lambda=p.softmax_lambda, softmax_beta=p.softmax_beta,
                               lambdamart_sigma=p.lambdamart_sigma, lambdamart_top=p.lambdamart_top,
-                              lambdamart_norm=p.lambdamart_norm, lambdamart_metric=p.lambdamart_metric)
+                              lambdamart_norm=p.lambdamart_norm, lambdamart_metric=p.lambdamart_metric,
+                              yeti_permutations=p.yeti_permutations, yeti_decay=p.yeti_decay)
     if not ok:
         raise RuntimeError(f"device declined: {rt.decline_reason}")
     T, D = p.iterations, p.depth
@@ -277,7 +281,7 @@ def fit_ranking(float_columns: Sequence[np.ndarray], borders: Sequence[Sequence[
                 sf[it, l], sb[it, l] = f, b
             raw[it] = tree.leaf_values
             leaf_w = np.bincount(tree.leaf_of.astype(np.int64), weights=doc_w, minlength=L)
-            lv[it] = normalize_leaf_values(p.loss in ("PairLogit", "PairLogitPairwise"), lr, leaf_w,
+            lv[it] = normalize_leaf_values(p.loss in ("PairLogit", "PairLogitPairwise", "YetiRank"), lr, leaf_w,
                                            tree.leaf_values)
             if staged:
                 st[it] = rt.resident_approx()[0]

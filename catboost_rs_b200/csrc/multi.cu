@@ -487,7 +487,7 @@ __global__ void mc_apply_pending_kernel(int64_t n, int K, int L, double* __restr
 // ---- ranking mode (grouped losses, K = 1) ----------------------------------
 
 enum : int { kRankQueryRmse = 0, kRankPairLogit = 1, kRankPairLogitPairwise = 2, kRankQuerySoftMax = 3,
-             kRankLambdaMart = 4 };
+             kRankLambdaMart = 4, kRankYetiRank = 5 };
 
 // Per-loss parameters of rk_der_kernel.  LambdaMart's position denominators
 // log2(2 + pos) (as log(x) * log2(e), ranking_der.rs:456-467) and each group's
@@ -743,6 +743,102 @@ __global__ void rk_newton_kernel(int L, int pairwise, int gradient, const unsign
         }
         leaf_lrv[q] = __dmul_rn(v, lr);
     }
+}
+
+// ---- YetiRank: per-tree pair sampling on the device --------------------------
+
+// sample_pairs (crates/cb-train/src/yetirank.rs:75-171), one thread per group:
+// per permutation one TFastRng64 draw per document (cast to f32, ratio
+// u / (1.000001 - u) in f32) multiplies exp(approx), a stable descending sort,
+// and the Classic decayed weights 0.15 * decay^k * |rel_a - rel_b| (f32) go to
+// the higher-relevance document's row of the group's dense f32 matrix
+// cw[winner][loser].  idx / boot are n-sized scratch indexed by object.
+__global__ void rk_yeti_sample_kernel(int n_groups, const int64_t* __restrict__ goff, const double* __restrict__ ap,
+                                      const double* __restrict__ target, int perms, double decay,
+                                      const uint64_t* __restrict__ seeds, const int64_t* __restrict__ cwoff,
+                                      float* __restrict__ cw, int32_t* __restrict__ idx, double* __restrict__ boot) {
+    const int gi = blockIdx.x * blockDim.x + threadIdx.x;
+    if (gi >= n_groups) return;
+    const int64_t b = goff[gi], g = goff[gi + 1] - b;
+    float* cwg = cw + cwoff[gi];
+    for (int64_t k = 0; k < g * g; ++k) cwg[k] = 0.0f;
+    if (g == 0) return;
+    Rng64 r = Rng64::from_seed(seeds[gi]);
+    int32_t* ix = idx + b;
+    double* bt = boot + b;
+    for (int p = 0; p < perms; ++p) {
+        for (int64_t i = 0; i < g; ++i) {
+            ix[i] = (int32_t)i;
+            const float u = __double2float_rn(real1(r));
+            const float ratio = __fdiv_rn(u, __fsub_rn(1.000001f, u));
+            bt[i] = __dmul_rn(exp(ap[b + i]), (double)ratio);
+        }
+        for (int64_t i = 1; i < g; ++i) {  // stable insertion sort, descending
+            const int32_t key = ix[i];
+            int64_t j = i - 1;
+            while (j >= 0 && bt[ix[j]] < bt[key]) {
+                ix[j + 1] = ix[j];
+                --j;
+            }
+            ix[j + 1] = key;
+        }
+        double dc = 1.0;
+        for (int64_t d = 1; d < g; ++d) {
+            const int32_t first = ix[d - 1], second = ix[d];
+            const float rf = __double2float_rn(target[b + first]), rs = __double2float_rn(target[b + second]);
+            const float pw = __double2float_rn(__dmul_rn(__dmul_rn(0.15, dc), (double)fabsf(__fsub_rn(rf, rs))));
+            if (rf > rs) cwg[first * g + second] = __fadd_rn(cwg[first * g + second], pw);
+            else if (rf < rs) cwg[second * g + first] = __fadd_rn(cwg[second * g + first], pw);
+            dc = __dmul_rn(dc, decay);
+        }
+    }
+}
+
+// The PairLogit der over one phase's sampled pairs (pairlogit_group_der,
+// ranking_der.rs:400-440), winner rows ascending, losers ascending, pair
+// weight (qw * cw / perms) in f32; eff (when given) gets the pairwise weights
+// (calc_pairwise_weights, boosting.rs:1761-1780) in the same order.
+__global__ void rk_yeti_der_kernel(int n_groups, const int64_t* __restrict__ goff, const double* __restrict__ ap,
+                                   const double* __restrict__ gw, int perms, const int64_t* __restrict__ cwoff,
+                                   const float* __restrict__ cw, double* __restrict__ d1, double* __restrict__ d2,
+                                   double* __restrict__ eff, McState* __restrict__ ms) {
+    const int gi = blockIdx.x * blockDim.x + threadIdx.x;
+    if (gi >= n_groups) return;
+    const int64_t b = goff[gi], g = goff[gi + 1] - b;
+    const float* cwg = cw + cwoff[gi];
+    const float qw = __double2float_rn(gw[gi]), den = (float)perms;
+    for (int64_t i = b; i < b + g; ++i) {
+        d1[i] = 0.0;
+        d2[i] = 0.0;
+        if (eff) eff[i] = 0.0;
+    }
+    bool finite = true;
+    for (int64_t wl = 0; wl < g; ++wl) {
+        double wd = 0.0, wd2 = 0.0;
+        const double ew = exp(ap[b + wl]);
+        for (int64_t ll = 0; ll < g; ++ll) {
+            const float wf = __fdiv_rn(__fmul_rn(qw, cwg[wl * g + ll]), den);
+            if (wf == 0.0f) continue;
+            const double c = (double)wf;
+            const double el = exp(ap[b + ll]);
+            const double dn = __dadd_rn(el, ew);
+            const double p = dn > 0.0 ? __ddiv_rn(el, dn) : 0.5;
+            const double cp = __dmul_rn(c, p);
+            const double t = __dmul_rn(cp, __dsub_rn(p, 1.0));
+            wd = __dadd_rn(wd, cp);
+            wd2 = __dadd_rn(wd2, t);
+            d1[b + ll] = __dsub_rn(d1[b + ll], cp);
+            d2[b + ll] = __dadd_rn(d2[b + ll], t);
+            if (eff) {
+                eff[b + wl] = __dadd_rn(eff[b + wl], c);
+                eff[b + ll] = __dadd_rn(eff[b + ll], c);
+            }
+        }
+        d1[b + wl] = __dadd_rn(d1[b + wl], wd);
+        d2[b + wl] = __dadd_rn(d2[b + wl], wd2);
+    }
+    for (int64_t i = b; i < b + g; ++i) finite &= isfinite(d1[i]) && isfinite(d2[i]);
+    if (!finite) atomicOr(&ms->err, kMcErrNonFinite);
 }
 
 // ---- PairLogitPairwise: pairwise split scoring and Cholesky pairwise leaves
@@ -1091,9 +1187,29 @@ struct cbgpu_multi_session {
     std::vector<int64_t> h_goff;
     double *d_lmden = nullptr, *d_lmideal = nullptr;
     int32_t* d_lmorder = nullptr;
+    // YetiRank: the seeder's context stream, group weights, per-tree query
+    // seeds (deriv, learning fold, leaf values), the dense per-group pair
+    // matrices, sort scratch, the learning-fold approximant and its deltas
+    McRng yeti_rng;
+    int yeti_perms = 10;
+    double yeti_decay = 0.85;
+    double* d_gw = nullptr;
+    uint64_t *d_yseeds = nullptr, *h_yseeds = nullptr;
+    int64_t* d_cwoff = nullptr;
+    float* d_cw = nullptr;
+    double *d_yboot = nullptr, *d_lapprox = nullptr, *d_ylf_raw = nullptr, *d_ylf_lrv = nullptr;
 
     ~cbgpu_multi_session() {
         if (st) cudaStreamSynchronize(st);
+        cudaFree(d_gw);
+        cudaFree(d_yseeds);
+        if (h_yseeds) cudaFreeHost(h_yseeds);
+        cudaFree(d_cwoff);
+        cudaFree(d_cw);
+        cudaFree(d_yboot);
+        cudaFree(d_lapprox);
+        cudaFree(d_ylf_raw);
+        cudaFree(d_ylf_lrv);
         cudaFree(d_lmden);
         cudaFree(d_lmideal);
         cudaFree(d_lmorder);
@@ -1319,6 +1435,7 @@ int cbgpu_rank_begin_raw(const cbgpu_begin_args* a, const int64_t* group_offsets
     else if (a->loss == CBGPU_LOSS_PAIRLOGIT_PAIRWISE) mode = kRankPairLogitPairwise;
     else if (a->loss == CBGPU_LOSS_QUERYSOFTMAX) mode = kRankQuerySoftMax;
     else if (a->loss == CBGPU_LOSS_LAMBDAMART) mode = kRankLambdaMart;
+    else if (a->loss == CBGPU_LOSS_YETIRANK) mode = kRankYetiRank;
     else return mfail(CBGPU_DECLINED, "rank_begin: loss %d is not a covered grouped loss", a->loss);
     const double l2_leaf_reg = params && params->l2_leaf_reg >= 0.0 ? params->l2_leaf_reg : a->scaled_l2;
     const double sm_lambda = params ? params->softmax_lambda : 0.01;
@@ -1328,6 +1445,20 @@ int cbgpu_rank_begin_raw(const cbgpu_begin_args* a, const int64_t* group_offsets
         return mfail(CBGPU_ERR_INVALID, "rank_begin: QuerySoftMax needs lambda >= 0 and beta > 0, finite");
     const double lm_sigma = params ? params->lambdamart_sigma : 1.0;
     const int64_t lm_top = params ? params->lambdamart_top : -1;
+    const int yeti_perms = params ? params->yeti_permutations : 10;
+    const double yeti_decay = params ? params->yeti_decay : 0.85;
+    if (mode == kRankYetiRank) {
+        if (yeti_perms < 1 || !std::isfinite(yeti_decay))
+            return mfail(CBGPU_ERR_INVALID, "rank_begin: YetiRank needs permutations >= 1 and a finite decay");
+        int64_t cells = 0;
+        for (int g = 0; g < n_groups; ++g) {
+            const int64_t sz = group_offsets[g + 1] - group_offsets[g];
+            cells += sz * sz;
+        }
+        if (cells > ((int64_t)1 << 31))
+            return mfail(CBGPU_DECLINED, "rank_begin: YetiRank pair matrices need %lld cells (> 2^31)",
+                         (long long)cells);
+    }
     if (mode == kRankLambdaMart) {
         if (params && params->lambdamart_metric != 0 && params->lambdamart_metric != 1)
             return mfail(CBGPU_DECLINED, "rank_begin: LambdaMart covers the NDCG / DCG metrics");
@@ -1427,12 +1558,45 @@ int cbgpu_rank_begin_raw(const cbgpu_begin_args* a, const int64_t* group_offsets
         s->lm_top = lm_top;
         s->lm_norm = params ? (params->lambdamart_norm ? 1 : 0) : 1;
         s->h_goff.assign(group_offsets, group_offsets + n_groups + 1);
+        s->yeti_perms = yeti_perms;
+        s->yeti_decay = yeti_decay;
+        s->yeti_rng.r = Rng64::from_seed(a->rng_seed);
         rc = mdalloc(&s->d_goff, (size_t)n_groups + 1);
         if (!rc) rc = mdalloc(&s->d_cstart, (size_t)n + 1);
         if (!rc) rc = mdalloc(&s->d_closer, closer.size());
         if (!rc) rc = mdalloc(&s->d_eff, (size_t)n);
         if (!rc) rc = mdalloc(&s->d_der2, (size_t)n);
         if (!rc) rc = mdalloc(&s->d_tgt, (size_t)n);
+        if (!rc && mode == kRankYetiRank) {
+            // group weight: the mean member weight (query_info.rs:180-187)
+            std::vector<double> gw((size_t)n_groups);
+            std::vector<int64_t> cwoff((size_t)n_groups);
+            int64_t cells = 0;
+            for (int g = 0; g < n_groups; ++g) {
+                const int64_t b = group_offsets[g], e = group_offsets[g + 1];
+                double acc = 0.0;
+                for (int64_t i = b; i < e; ++i) acc += a->weight ? a->weight[i] : 1.0;
+                gw[(size_t)g] = e > b ? acc / (double)(e - b) : 1.0;
+                cwoff[(size_t)g] = cells;
+                cells += (e - b) * (e - b);
+            }
+            rc = mdalloc(&s->d_gw, (size_t)n_groups);
+            if (!rc) rc = mdalloc(&s->d_yseeds, 3 * (size_t)n_groups);
+            if (!rc) rc = mhalloc(&s->h_yseeds, 3 * (size_t)n_groups);
+            if (!rc) rc = mdalloc(&s->d_cwoff, (size_t)n_groups);
+            if (!rc) rc = mdalloc(&s->d_cw, (size_t)std::max<int64_t>(cells, 1));
+            if (!rc) rc = mdalloc(&s->d_lmorder, (size_t)n);
+            if (!rc) rc = mdalloc(&s->d_yboot, (size_t)n);
+            if (!rc) rc = mdalloc(&s->d_lapprox, (size_t)n);
+            if (!rc) rc = mdalloc(&s->d_ylf_raw, (size_t)1 << a->depth);
+            if (!rc) rc = mdalloc(&s->d_ylf_lrv, (size_t)1 << a->depth);
+            if (!rc && (cudaMemcpy(s->d_gw, gw.data(), sizeof(double) * gw.size(), cudaMemcpyHostToDevice) !=
+                            cudaSuccess ||
+                        cudaMemcpy(s->d_cwoff, cwoff.data(), sizeof(int64_t) * cwoff.size(),
+                                   cudaMemcpyHostToDevice) != cudaSuccess ||
+                        cudaMemset(s->d_lapprox, 0, sizeof(double) * (size_t)n) != cudaSuccess))
+                rc = mfail(CBGPU_ERR_CUDA, "rank_begin: upload failed");
+        }
         if (!rc && mode == kRankLambdaMart) {
             int64_t maxg = 1;
             for (int g = 0; g < n_groups; ++g) maxg = std::max(maxg, group_offsets[g + 1] - group_offsets[g]);
@@ -1565,9 +1729,45 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
     MCU(cudaMemcpyAsync(s->d_tp, s->h_tp, sizeof(TreeParams), cudaMemcpyHostToDevice, st));
     MCU(cudaMemsetAsync(s->d_ms, 0, sizeof(McState), st));
     const unsigned g = grid_for(n);
+    const bool yeti = s->rank_mode == kRankYetiRank;
+    const unsigned yg = (unsigned)((s->n_groups + 127) / 128);
+    if (yeti) {
+        // YetiRankTreeSeeder::next_tree (yetirank.rs:340-430) on the host: the
+        // per-group query seeds of the three resamples of this tree
+        const int G = s->n_groups;
+        McRng& yr = s->yeti_rng;
+        auto first_gen = [](uint64_t seed) { Rng64 t = Rng64::from_seed(seed); return t.gen(); };
+        auto fill = [&](uint64_t recalc, uint64_t* out) {
+            Rng64 t = Rng64::from_seed(recalc);
+            for (int q = 0; q < G; ++q) out[q] = first_gen(t.gen());
+        };
+        (void)yr.gen();  // structure-fold selection
+        const uint64_t drs = first_gen(yr.gen());
+        for (int l = 0; l < D; ++l) {
+            for (int f = 0; f < F; ++f) (void)yr.real1();
+            (void)yr.gen();
+            for (int f = 0; f < F; ++f) (void)yr.std_normal();
+        }
+        const uint64_t lrs = first_gen(first_gen(yr.gen()));
+        const uint64_t vb = yr.gen();
+        fill(drs, s->h_yseeds);
+        fill(lrs, s->h_yseeds + G);
+        fill(vb, s->h_yseeds + 2 * (size_t)G);
+        MCU(cudaMemcpyAsync(s->d_yseeds, s->h_yseeds, sizeof(uint64_t) * 3 * (size_t)G, cudaMemcpyHostToDevice, st));
+    }
     if (s->rank_mode >= 0) {
         if (s->pending)
             mc_apply_pending_kernel<<<g, kMcThreads, 0, st>>>(n, 1, L, s->approx, s->leaf, s->leaf_lrv);
+    }
+    if (yeti) {
+        // gradient / split ders and the histogram's pairwise weights from pairs
+        // sampled off the learning-fold approximant
+        rk_yeti_sample_kernel<<<yg, 128, 0, st>>>(s->n_groups, s->d_goff, s->d_lapprox, s->d_tgt, s->yeti_perms,
+                                                 s->yeti_decay, s->d_yseeds, s->d_cwoff, s->d_cw, s->d_lmorder,
+                                                 s->d_yboot);
+        rk_yeti_der_kernel<<<yg, 128, 0, st>>>(s->n_groups, s->d_goff, s->d_lapprox, s->d_gw, s->yeti_perms,
+                                              s->d_cwoff, s->d_cw, s->wd1, s->d_der2, s->d_eff, s->d_ms);
+    } else if (s->rank_mode >= 0) {
         rk_der_kernel<<<(unsigned)((s->n_groups + 127) / 128), 128, 0, st>>>(
             s->n_groups, s->rank_mode, s->d_goff, s->d_cstart, s->d_closer, s->approx, s->d_tgt, s->weight,
             RkLossParams{s->sm_lambda, s->sm_beta, s->lm_sigma, s->lm_top, s->lm_norm, s->d_lmden, s->d_lmideal,
@@ -1629,6 +1829,13 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
         rk_leafmax_kernel<<<g, kMcThreads, 0, st>>>(n, s->wd1, s->d_der2, s->weight, s->d_ms);
         rk_leafshift_kernel<<<1, 1, 0, st>>>(n, s->d_ms);
         MCU(cudaMemsetAsync(s->sums, 0, sizeof(unsigned long long) * 3 * (size_t)L, st));
+        if (yeti) {  // the stored leaves come from pairs sampled off the model approximant
+            rk_yeti_sample_kernel<<<yg, 128, 0, st>>>(s->n_groups, s->d_goff, s->approx, s->d_tgt, s->yeti_perms,
+                                                     s->yeti_decay, s->d_yseeds + 2 * (size_t)s->n_groups, s->d_cwoff,
+                                                     s->d_cw, s->d_lmorder, s->d_yboot);
+            rk_yeti_der_kernel<<<yg, 128, 0, st>>>(s->n_groups, s->d_goff, s->approx, s->d_gw, s->yeti_perms,
+                                                  s->d_cwoff, s->d_cw, s->wd1, s->d_der2, nullptr, s->d_ms);
+        }
         const int gradient = s->rank_mode == kRankQuerySoftMax ? 1 : 0;
         rk_leafsum_kernel<<<g, kMcThreads, 0, st>>>(n, L, s->wd1, s->d_der2, s->weight, s->leaf, gradient, s->sums,
                                                     s->d_ms);
@@ -1639,8 +1846,23 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
             rk_pairleaf_kernel<<<1, kPwThreads, 0, st>>>(L, s->d_pwsum, s->sums, s->d_ms, s->raw_l2, s->lr,
                                                          s->d_pwscratch, s->leaf_raw, s->leaf_lrv);
         } else {
-            rk_newton_kernel<<<1, 1, 0, st>>>(L, s->rank_mode == kRankPairLogit ? 1 : 0, gradient, s->sums, s->d_ms,
-                                              s->l2, s->lr, s->leaf_raw, s->leaf_lrv);
+            rk_newton_kernel<<<1, 1, 0, st>>>(L, (s->rank_mode == kRankPairLogit || yeti) ? 1 : 0, gradient, s->sums,
+                                              s->d_ms, s->l2, s->lr, s->leaf_raw, s->leaf_lrv);
+        }
+        if (yeti) {
+            // the learning fold: its own resample, Newton deltas x lr, no centring
+            rk_yeti_sample_kernel<<<yg, 128, 0, st>>>(s->n_groups, s->d_goff, s->d_lapprox, s->d_tgt, s->yeti_perms,
+                                                     s->yeti_decay, s->d_yseeds + (size_t)s->n_groups, s->d_cwoff,
+                                                     s->d_cw, s->d_lmorder, s->d_yboot);
+            rk_yeti_der_kernel<<<yg, 128, 0, st>>>(s->n_groups, s->d_goff, s->d_lapprox, s->d_gw, s->yeti_perms,
+                                                  s->d_cwoff, s->d_cw, s->wd1, s->d_der2, nullptr, s->d_ms);
+            rk_leafmax_kernel<<<g, kMcThreads, 0, st>>>(n, s->wd1, s->d_der2, s->weight, s->d_ms);
+            rk_leafshift_kernel<<<1, 1, 0, st>>>(n, s->d_ms);
+            MCU(cudaMemsetAsync(s->sums, 0, sizeof(unsigned long long) * 3 * (size_t)L, st));
+            rk_leafsum_kernel<<<g, kMcThreads, 0, st>>>(n, L, s->wd1, s->d_der2, s->weight, s->leaf, 0, s->sums,
+                                                        s->d_ms);
+            rk_newton_kernel<<<1, 1, 0, st>>>(L, 0, 0, s->sums, s->d_ms, s->l2, s->lr, s->d_ylf_raw, s->d_ylf_lrv);
+            mc_apply_pending_kernel<<<g, kMcThreads, 0, st>>>(n, 1, L, s->d_lapprox, s->leaf, s->d_ylf_lrv);
         }
         MCU(cudaGetLastError());
     } else {

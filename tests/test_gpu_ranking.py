@@ -1,5 +1,5 @@
-"""The grouped-loss (QueryRMSE, QuerySoftMax, LambdaMart, PairLogit, PairLogitPairwise) device mode against upstream
-and the oracle.
+"""The grouped-loss (QueryRMSE, QuerySoftMax, LambdaMart, YetiRank, PairLogit, PairLogitPairwise) device mode against
+upstream and the oracle.
 
 The device mode (csrc/multi.cu, cbgpu_rank_begin_raw) reproduces cb-train's
 grouped CPU branch: grouped ders (crates/cb-compute/src/ranking_der.rs),
@@ -34,7 +34,8 @@ def cb():
     return cb
 
 
-@pytest.mark.parametrize("loss", ["QueryRMSE", "PairLogit", "PairLogitPairwise", "QuerySoftMax", "LambdaMart"])
+@pytest.mark.parametrize("loss", ["QueryRMSE", "PairLogit", "PairLogitPairwise", "QuerySoftMax", "LambdaMart",
+                                  "YetiRank"])
 def test_ranking_fixture(cb, loss):
     z = np.load(GOLDEN)
     p = json.loads(str(z[f"{loss}__params"]))
@@ -44,7 +45,8 @@ def test_ranking_fixture(cb, loss):
                       l2_leaf_reg=p["l2_leaf_reg"], random_seed=p["random_seed"], boost_from_average=False,
                       softmax_lambda=p.get("softmax_lambda", 0.01), softmax_beta=p.get("softmax_beta", 1.0),
                       lambdamart_sigma=p.get("lambdamart_sigma", 1.0), lambdamart_top=p.get("lambdamart_top", -1),
-                      lambdamart_norm=p.get("lambdamart_norm", True))
+                      lambdamart_norm=p.get("lambdamart_norm", True), yeti_permutations=p.get("yeti_permutations", 10),
+                      yeti_decay=p.get("yeti_decay", 0.85))
     m = cb.fit_ranking([X[:, f].copy() for f in range(X.shape[1])], borders, z["y"], z["group_offsets"], fp,
                        pairs=z["pairs"], staged=True)
     np.testing.assert_array_equal(m.split_feature, z[f"{loss}__split_feature"])
@@ -130,6 +132,31 @@ def test_lambdamart_matches_oracle(cb, top, norm, sigma):
                              lambdamart_norm=norm)
     np.testing.assert_array_equal(m.split_feature, o.split_feature)
     np.testing.assert_array_equal(m.split_bin, o.split_bin)
+    assert np.max(np.abs(m.leaf_values - o.leaf_values)) <= TOL
+    assert np.max(np.abs(m.staged - o.staged)) <= TOL
+
+
+@pytest.mark.parametrize("perms,decay,weighted", [(10, 0.85, False), (3, 0.5, True)])
+def test_yetirank_matches_oracle(cb, perms, decay, weighted):
+    # pairs resampled on the device every tree from the host seeder's query seeds;
+    # the learning-fold approximant drives the splits, the model's the leaves
+    X, y, offsets, pairs = _ranking_data(80, 8, 57)
+    n, F = X.shape
+    w = None
+    if weighted:  # one weight per group: the group weight is the members' mean
+        gw = np.random.RandomState(2).choice([0.5, 1.0, 2.0], size=offsets.size - 1)
+        w = np.repeat(gw, np.diff(offsets))
+    borders = [oracle.select_borders(X[:, f], 48) for f in range(F)]
+    fp = cb.FitParams(loss="YetiRank", depth=5, iterations=4, learning_rate=0.3, l2_leaf_reg=1.0, random_seed=11,
+                      boost_from_average=False, yeti_permutations=perms, yeti_decay=decay)
+    m = cb.fit_ranking([X[:, f].copy() for f in range(F)], borders, y, offsets, fp, weights=w, staged=True)
+    bins = oracle.quantize(X.T.copy(), borders)
+    o = oracle.train_ranking(bins, [len(b) for b in borders], y, offsets, loss="YetiRank", depth=5, iterations=4,
+                             learning_rate=0.3, l2_leaf_reg=1.0, random_seed=11, weights=w,
+                             yeti_permutations=perms, yeti_decay=decay)
+    np.testing.assert_array_equal(m.split_feature, o.split_feature)
+    np.testing.assert_array_equal(m.split_bin, o.split_bin)
+    assert np.max(np.abs(m.raw_leaf_values - o.raw_leaf_values)) <= TOL
     assert np.max(np.abs(m.leaf_values - o.leaf_values)) <= TOL
     assert np.max(np.abs(m.staged - o.staged)) <= TOL
 
