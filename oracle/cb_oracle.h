@@ -188,7 +188,7 @@ void orc_solve_symmetric_newton(const double* sum_der, const double* sum_der2_pa
 
 /* ---- grouped (ranking) losses, pointwise histograms -------------------- */
 enum { ORC_RANK_QUERYRMSE = 0, ORC_RANK_PAIRLOGIT = 1, ORC_RANK_PAIRLOGIT_PAIRWISE = 2, ORC_RANK_QUERYSOFTMAX = 3,
-       ORC_RANK_LAMBDAMART = 4, ORC_RANK_YETIRANK = 5 };
+       ORC_RANK_LAMBDAMART = 4, ORC_RANK_YETIRANK = 5, ORC_RANK_STOCHASTICRANK = 6 };
 
 /* The greedy oblivious search of the scalar loop, exported for the grouped
  * loop: returns the splits taken; leaf_of gets the final leaf ids. */
@@ -222,6 +222,10 @@ typedef struct {
     int32_t lambdamart_norm;       /* LambdaMart norm (default 1) */
     int32_t yeti_permutations;     /* YetiRank permutations (default 10) */
     double yeti_decay;             /* YetiRank decay (default 0.85) */
+    int32_t srank_ndcg;            /* StochasticRank metric: 1 NDCG, 0 DCG */
+    double srank_sigma;            /* StochasticRank sigma (default 1.0) */
+    double srank_mu;               /* StochasticRank mu (default 0.0) */
+    int32_t srank_num_estimations; /* StochasticRank num_estimations (default 1) */
 } orc_rank_args;
 
 /* YetiRank's sampler for one group (sample_pairs, crates/cb-train/src/

@@ -1,8 +1,8 @@
 /*
  * cb_oracle_rank.c -- CPU restatement of catboost_rs's grouped (ranking)
  * losses on the oblivious loop: QueryRMSE, QuerySoftMax, LambdaMart (NDCG /
- * DCG), PairLogit and YetiRank on pointwise histograms, and PairLogitPairwise
- * with the pairwise split scoring and
+ * DCG), StochasticRank (DCG / NDCG), PairLogit and YetiRank on pointwise
+ * histograms, and PairLogitPairwise with the pairwise split scoring and
  * Cholesky leaves (crates/cb-compute/src/ranking_der.rs, pairwise_scoring.rs,
  * crates/cb-train/src/boosting.rs grouped branch, pairwise_leaves.rs,
  * tree.rs:3740-3960, query_info.rs).
@@ -147,6 +147,146 @@ static void lambdamart_group(const double* ap, const double* tg, int64_t cnt, do
         for (int64_t i = 0; i < cnt; ++i) {
             d1[i] *= norma;
             d2[i] *= norma;
+        }
+    }
+}
+
+/* ---- StochasticRank (ranking_der.rs:640-1000) --------------------------- */
+
+/* normal_density (ranking_der.rs:640-655) */
+static double srank_density(double x, double mean, double sigma) {
+    const double t = (x - mean) / sigma;
+    const double z = t * t;
+    return exp(-z / 2.0) * 0.398942280401432677939946 / sigma;
+}
+
+/* calc_dcg_metric_diff (ranking_der.rs:920-965) */
+static double srank_metric_diff(int64_t old_pos, int64_t new_pos, const double* tg, const int64_t* order,
+                                const double* pw, const double* cs, const double* csu, const double* csl) {
+    const double gain = tg[order[old_pos]];
+    const double doc_diff = gain * (pw[new_pos] - pw[old_pos]);
+    double mid;
+    if (new_pos < old_pos) {
+        const double old_mid = cs[old_pos] - cs[new_pos];
+        const double new_mid = csl[old_pos] - csl[new_pos];
+        mid = new_mid - old_mid;
+    } else {
+        const double old_mid = cs[new_pos + 1] - cs[old_pos + 1];
+        const double new_mid = csu[new_pos + 1] - csu[old_pos + 1];
+        mid = new_mid - old_mid;
+    }
+    return doc_diff + mid;
+}
+
+/* stochastic_rank_group_der (ranking_der.rs:710-910), DCG / NDCG, the whole
+ * group as the top; der2 = 0.  ws: 9 * cnt + 3 doubles, order: cnt. */
+static void stochastic_rank_group(const double* ap_raw, const double* tg, int64_t cnt, int is_ndcg, double sigma_p,
+                                  double mu, int32_t num_est, uint64_t seed, double* ws, int64_t* order, double* d1,
+                                  double* d2) {
+    for (int64_t i = 0; i < cnt; ++i) {
+        d1[i] = 0.0;
+        d2[i] = 0.0;
+    }
+    if (cnt <= 1) return;
+    if (num_est < 1) num_est = 1;
+    double* ap = ws;
+    double* sh = ap + cnt;
+    double* pw = sh + cnt;
+    double* noise = pw + cnt;
+    double* sc = noise + cnt;
+    double* cs = sc + cnt;
+    double* csu = cs + cnt + 1;
+    double* csl = csu + cnt + 1;
+    double* tmp = csl + cnt + 1;
+    const double am = orc_sum_f64(ap_raw, cnt) / (double)cnt; /* group-mean centring */
+    for (int64_t i = 0; i < cnt; ++i) ap[i] = ap_raw[i] - am;
+    for (int64_t i = 0; i < cnt; ++i) sh[i] = ap[i] - sigma_p * mu * tg[i];
+    const double avs = orc_sum_f64(sh, cnt) / (double)cnt;
+    for (int64_t i = 0; i < cnt; ++i) sh[i] -= avs;
+    /* compute_dcg_pos_weights (ranking_der.rs:659-690) */
+    for (int64_t p = 0; p < cnt; ++p) pw[p] = 1.0 / lm_den(p);
+    if (is_ndcg) {
+        for (int64_t i = 0; i < cnt; ++i) tmp[i] = tg[i];
+        for (int64_t i = 1; i < cnt; ++i) {
+            const double key = tmp[i];
+            int64_t j = i - 1;
+            while (j >= 0 && tmp[j] < key) {
+                tmp[j + 1] = tmp[j];
+                --j;
+            }
+            tmp[j + 1] = key;
+        }
+        double ideal = 0.0;
+        for (int64_t p = 0; p < cnt; ++p) ideal += tmp[p] * pw[p];
+        if (ideal > DBL_EPSILON)
+            for (int64_t p = 0; p < cnt; ++p) pw[p] /= ideal;
+    }
+    orc_rng rng;
+    orc_rng_from_seed(&rng, seed);
+    const double sigma = sigma_p * sqrt((double)cnt / ((double)cnt - 1.0));
+    for (int32_t s = 0; s < num_est; ++s) {
+        for (int64_t d = 0; d < cnt; ++d) {
+            noise[d] = orc_std_normal(&rng);
+            sc[d] = sh[d] + sigma_p * noise[d];
+        }
+        const double noise_sum = orc_sum_f64(noise, cnt);
+        for (int64_t i = 0; i < cnt; ++i) order[i] = i;
+        for (int64_t i = 1; i < cnt; ++i) { /* stable, descending by score */
+            const int64_t key = order[i];
+            int64_t j = i - 1;
+            while (j >= 0 && sc[order[j]] < sc[key]) {
+                order[j + 1] = order[j];
+                --j;
+            }
+            order[j + 1] = key;
+        }
+        /* CalcDCGCumulativeStatistics */
+        for (int64_t p = 0; p <= cnt; ++p) {
+            cs[p] = 0.0;
+            csu[p] = 0.0;
+            csl[p] = 0.0;
+        }
+        for (int64_t p = 0; p < cnt; ++p) {
+            const double gain = tg[order[p]];
+            cs[p + 1] = cs[p] + gain * pw[p];
+            if (p + 1 < cnt) csl[p + 1] = csl[p] + gain * pw[p + 1];
+            if (p > 0) csu[p + 1] = csu[p] + gain * pw[p - 1];
+        }
+        csl[cnt] = csl[cnt - 1];
+        for (int64_t p = 0; p < cnt; ++p) {
+            const int64_t doc = order[p];
+            const double score = sc[doc], a = ap[doc];
+            const double mean = a + (noise_sum - (score - a)) / ((double)cnt - 1.0);
+            double der_sum = 0.0;
+            for (int64_t np = 0; np < cnt; ++np) {
+                if (np == p) continue;
+                const double md = srank_metric_diff(p, np, tg, order, pw, cs, csu, csl);
+                double dd;
+                if (np == 0) dd = srank_density(sc[order[0]], mean, sigma);
+                else if (np + 1 == cnt) dd = -srank_density(sc[order[cnt - 1]], mean, sigma);
+                else if (np < p) dd = srank_density(sc[order[np]], mean, sigma) - srank_density(sc[order[np - 1]], mean, sigma);
+                else dd = srank_density(sc[order[np + 1]], mean, sigma) - srank_density(sc[order[np]], mean, sigma);
+                der_sum += md * dd;
+            }
+            d1[doc] += der_sum / (double)num_est;
+        }
+    }
+    /* SFA: remove the mean der, then project out the approx direction */
+    const double avg_der = orc_sum_f64(d1, cnt) / (double)cnt;
+    for (int64_t i = 0; i < cnt; ++i) d1[i] -= avg_der;
+    if (cnt > 2) {
+        const double aa = orc_sum_f64(ap, cnt) / (double)cnt;
+        for (int64_t i = 0; i < cnt; ++i) {
+            sh[i] = ap[i] - aa; /* zero-mean approx */
+            tmp[i] = sh[i] * sh[i];
+        }
+        const double nr = sqrt(orc_sum_f64(tmp, cnt)) + 0.01;
+        const double norm_sqr = nr * nr;
+        for (int64_t i = 0; i < cnt; ++i) tmp[i] = d1[i] * sh[i];
+        const double dot = orc_sum_f64(tmp, cnt);
+        if (norm_sqr > 0.0) {
+            const double k = 1.0 * dot / norm_sqr;
+            for (int64_t i = 0; i < cnt; ++i) d1[i] -= k * sh[i];
         }
     }
 }
@@ -389,6 +529,75 @@ static int train_yetirank(const orc_rank_args* a, orc_rank_out* o, int32_t NB) {
     return rc;
 }
 
+/* The StochasticRank loop: the YetiRank seeder's derivative and leaf-value
+ * recalc seeds per tree (boosting.rs:5065-5100, 7331-7345, 8135-8170), each
+ * group's noise seeded with base + group index; one approximant; Gradient
+ * leaves over unit weights; no centring. */
+static int train_stochasticrank(const orc_rank_args* a, orc_rank_out* o, int32_t NB) {
+    const int64_t n = a->n;
+    const int32_t F = a->n_features, D = a->depth, L = 1 << D, G = a->n_groups;
+    double* w = (double*)calloc((size_t)n + 1, sizeof(double));
+    for (int64_t i = 0; i < n; ++i) w[i] = a->weights ? a->weights[i] : 1.0;
+    const double sum_w = orc_sum_f64(w, n);
+    const double scaled_l2 = n == 0 ? a->l2_leaf_reg : a->l2_leaf_reg * (sum_w / (double)n);
+    const double lr = (double)(float)a->learning_rate;
+    int64_t maxg = 1;
+    for (int32_t gi = 0; gi < G; ++gi)
+        if (a->group_offsets[gi + 1] - a->group_offsets[gi] > maxg) maxg = a->group_offsets[gi + 1] - a->group_offsets[gi];
+    double* ws = (double*)malloc(sizeof(double) * (size_t)(9 * maxg + 3));
+    int64_t* order = (int64_t*)malloc(sizeof(int64_t) * (size_t)maxg);
+    double* approx = (double*)calloc((size_t)n + 1, sizeof(double));
+    double* d1 = (double*)malloc(sizeof(double) * ((size_t)n + 1));
+    double* d2 = (double*)malloc(sizeof(double) * ((size_t)n + 1));
+    int32_t* leaf = (int32_t*)malloc(sizeof(int32_t) * ((size_t)n + 1));
+    double* lv = (double*)malloc(sizeof(double) * L);
+    double* cnt = (double*)malloc(sizeof(double) * L);
+    orc_rng seeder, unused;
+    orc_rng_from_seed(&seeder, a->random_seed);
+    orc_rng_from_seed(&unused, a->random_seed);
+    int rc = 0;
+    for (int32_t it = 0; it < a->iterations; ++it) {
+        uint64_t rs[3];
+        yeti_next_tree(&seeder, G, F, D, NULL, NULL, NULL, rs);
+        for (int32_t phase = 0; phase < 2; ++phase) {
+            const uint64_t base = phase == 0 ? rs[0] : rs[2];
+            for (int32_t gi = 0; gi < G; ++gi) {
+                const int64_t b = a->group_offsets[gi], e = a->group_offsets[gi + 1];
+                stochastic_rank_group(approx + b, a->target + b, e - b, a->srank_ndcg, a->srank_sigma, a->srank_mu,
+                                      a->srank_num_estimations, base + (uint64_t)gi, ws, order, d1 + b, d2 + b);
+            }
+            if (phase == 0) {
+                int32_t* tf = o->split_feature + (size_t)it * D;
+                int32_t* tb = o->split_bin + (size_t)it * D;
+                int32_t err = 0;
+                orc_search_tree(n, F, NB, D, a->score_function, a->bins_fm, a->border_counts, d1, w, scaled_l2, 0,
+                                &unused, tf, tb, leaf, &err);
+                if (err) {
+                    rc = -3;
+                    break;
+                }
+            }
+        }
+        if (rc) break;
+        for (int32_t q = 0; q < L; ++q) {
+            lv[q] = 0.0;
+            cnt[q] = 0.0;
+        }
+        for (int64_t i = 0; i < n; ++i) {
+            lv[leaf[i]] += d1[i];
+            cnt[leaf[i]] += 1.0;
+        }
+        for (int32_t q = 0; q < L; ++q) lv[q] = cnt[q] > 0.0 ? lv[q] / (cnt[q] + scaled_l2) : 0.0;
+        if (o->raw_leaf_values) memcpy(o->raw_leaf_values + (size_t)it * L, lv, sizeof(double) * L);
+        for (int32_t q = 0; q < L; ++q) lv[q] *= lr;
+        memcpy(o->leaf_values + (size_t)it * L, lv, sizeof(double) * L);
+        for (int64_t i = 0; i < n; ++i) approx[i] += lv[leaf[i]];
+        if (o->staged) memcpy(o->staged + (size_t)it * n, approx, sizeof(double) * (size_t)n);
+    }
+    free(w); free(ws); free(order); free(approx); free(d1); free(d2); free(leaf); free(lv); free(cnt);
+    return rc;
+}
+
 /* ---- pairwise scoring (crates/cb-compute/src/pairwise_scoring.rs) ------- */
 
 /* make_zero_average (pairwise_leaves.rs:202-212) */
@@ -583,6 +792,7 @@ int orc_train_ranking(const orc_rank_args* a, orc_rank_out* o) {
     for (int32_t f = 0; f < F; ++f)
         if (a->border_counts[f] + 1 > NB) NB = a->border_counts[f] + 1;
     if (a->loss == ORC_RANK_YETIRANK) return train_yetirank(a, o, NB);
+    if (a->loss == ORC_RANK_STOCHASTICRANK) return train_stochasticrank(a, o, NB);
     competitors cp = {NULL, NULL};
     const int pairlogit = a->loss == ORC_RANK_PAIRLOGIT || a->loss == ORC_RANK_PAIRLOGIT_PAIRWISE;
     if (pairlogit && build_competitors(a, &cp) != 0) {

@@ -82,7 +82,8 @@ class _RankArgs(C.Structure):
         ("learning_rate", C.c_double), ("l2_leaf_reg", C.c_double), ("score_function", C.c_int32),
         ("random_seed", C.c_uint64), ("softmax_lambda", C.c_double), ("softmax_beta", C.c_double),
         ("lambdamart_sigma", C.c_double), ("lambdamart_top", C.c_int64), ("lambdamart_norm", C.c_int32),
-        ("yeti_permutations", C.c_int32), ("yeti_decay", C.c_double),
+        ("yeti_permutations", C.c_int32), ("yeti_decay", C.c_double), ("srank_ndcg", C.c_int32),
+        ("srank_sigma", C.c_double), ("srank_mu", C.c_double), ("srank_num_estimations", C.c_int32),
     ]
 
 
@@ -91,7 +92,7 @@ class _RankOut(C.Structure):
                 ("raw_leaf_values", C.c_void_p), ("staged", C.c_void_p)]
 
 
-RANK_LOSS = {"QueryRMSE": 0, "PairLogit": 1, "PairLogitPairwise": 2, "QuerySoftMax": 3, "LambdaMart": 4, "YetiRank": 5}
+RANK_LOSS = {"QueryRMSE": 0, "PairLogit": 1, "PairLogitPairwise": 2, "QuerySoftMax": 3, "LambdaMart": 4, "YetiRank": 5, "StochasticRank": 6}
 
 
 def lib():
@@ -411,11 +412,13 @@ def train_ranking(bins_fm, border_counts, target, group_offsets, *, loss="QueryR
                   iterations=10, learning_rate=0.1, l2_leaf_reg=3.0, score_function="Cosine", random_seed=0,
                   weights=None, staged=True, softmax_lambda=0.01, softmax_beta=1.0, lambdamart_sigma=1.0,
                   lambdamart_top=-1, lambdamart_norm=True, yeti_permutations=10,
-                  yeti_decay=0.85) -> OracleRankFit:
+                  yeti_decay=0.85, srank_metric="DCG", srank_sigma=1.0, srank_mu=0.0,
+                  srank_num_estimations=1) -> OracleRankFit:
     """The reference's grouped-loss CPU loop: QueryRMSE / PairLogit (pointwise histograms, Newton
     leaves), QuerySoftMax (pointwise histograms, Gradient leaves), LambdaMart (NDCG lambdas, Newton
-    leaves), YetiRank (sampled pairs, Newton leaves, two approximants) and PairLogitPairwise (pairwise
-    scoring, Cholesky pairwise leaves)."""
+    leaves), YetiRank (sampled pairs, Newton leaves, two approximants), StochasticRank (Monte-Carlo
+    DCG / NDCG ders, Gradient leaves) and PairLogitPairwise (pairwise scoring, Cholesky pairwise
+    leaves)."""
     bins = np.ascontiguousarray(bins_fm, dtype=np.uint8)
     F, n = bins.shape
     bc = np.ascontiguousarray(border_counts, dtype=np.int32)
@@ -434,7 +437,8 @@ def train_ranking(bins_fm, border_counts, target, group_offsets, *, loss="QueryR
     args = _RankArgs(n, F, _p(bins), _p(bc), _p(t), _p(w), RANK_LOSS[loss], go.size - 1, _p(go), pw.size, _p(pw),
                      _p(pl), depth, iterations, learning_rate, l2_leaf_reg, SCORE[score_function], random_seed,
                      softmax_lambda, softmax_beta, lambdamart_sigma, lambdamart_top, int(bool(lambdamart_norm)),
-                     yeti_permutations, yeti_decay)
+                     yeti_permutations, yeti_decay, 1 if srank_metric == "NDCG" else 0, srank_sigma, srank_mu,
+                     srank_num_estimations)
     out = _RankOut(_p(sf), _p(sb), _p(lv), _p(raw), _p(st))
     rc = lib().orc_train_ranking(C.byref(args), C.byref(out))
     if rc != 0:

@@ -244,8 +244,9 @@ def ranking_fixtures(ref):
                   y=np.load(os.path.join(fx, "inputs/y.npy")).astype(np.float64), group_offsets=offsets,
                   pairs=np.load(os.path.join(fx, "inputs/pairs.npy")).astype(np.int64))
     losses = []
-    for loss in ("QueryRMSE", "PairLogit", "PairLogitPairwise", "QuerySoftMax", "LambdaMart", "YetiRank"):
-        d = {"YetiRank": "yetirank"}.get(loss, loss)
+    for loss in ("QueryRMSE", "PairLogit", "PairLogitPairwise", "QuerySoftMax", "LambdaMart", "YetiRank",
+                 "StochasticRank"):
+        d = {"YetiRank": "yetirank", "StochasticRank": "stochasticrank"}.get(loss, loss)
         cfg = json.loads(_read(os.path.join(fx, d, "config.json")))
         model = json.loads(_read(os.path.join(fx, d, "model.json")))
         mparams = model["model_info"].get("params")
@@ -267,7 +268,9 @@ def ranking_fixtures(ref):
             "lambdamart_sigma": float(lf.get("sigma", 1.0)), "lambdamart_top": int(lf.get("top", -1)),
             "lambdamart_norm": str(lf.get("norm", "true")).lower() == "true",
             "lambdamart_metric": str(lf.get("metric", "NDCG")),
-            "yeti_permutations": int(lf.get("permutations", 10)), "yeti_decay": float(lf.get("decay", 0.85))}))
+            "yeti_permutations": int(lf.get("permutations", 10)), "yeti_decay": float(lf.get("decay", 0.85)),
+            "srank_metric": str(lf.get("metric", "NDCG")), "srank_sigma": float(lf.get("sigma", 1.0)),
+            "srank_mu": float(lf.get("mu", 0.0)), "srank_num_estimations": int(lf.get("num_estimations", 1))}))
         losses.append(loss)
     # YetiRank's instrumented sampler log: one 3-document group (raw approx
     # [0.5, -0.3, 0.1], relevances [2, 0, 1], 10 permutations, decay 0.85,
@@ -285,6 +288,12 @@ def ranking_fixtures(ref):
         fx, "yetirank_pairwise/yetirank_pairwise_tree_rng_groundtruth.jsonl")).splitlines() if l.strip()]
     arrays["yeti_gt_recalc_seeds"] = np.array([e["random_seed"] for e in tr if e["event"] == "update_pairs"],
                                               dtype=np.uint64).reshape(-1, 3)
+    # StochasticRank's trainer noise log: per tree and phase each group's
+    # std_normal stream seeded with the recalc base + the group index
+    sn = [json.loads(l) for l in _read(os.path.join(
+        fx, "stochasticrank/stochasticrank_pertree_noise_groundtruth.jsonl")).splitlines() if l.strip()]
+    arrays["srank_gt_noise_seed"] = np.array([e["seed"] for e in sn], dtype=np.uint64)
+    arrays["srank_gt_noise"] = np.array([[e["sample"], e["doc"], e["count"], e["noise"]] for e in sn])
     np.savez_compressed(os.path.join(OUT, "ranking_corpus.npz"), **arrays)
     return ["ranking_corpus/" + l for l in losses]
 

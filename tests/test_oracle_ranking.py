@@ -1,5 +1,5 @@
-"""Pin the oracle's grouped-loss loop (QueryRMSE, PairLogit, PairLogitPairwise, QuerySoftMax, LambdaMart, YetiRank)
-to upstream.
+"""Pin the oracle's grouped-loss loop (QueryRMSE, PairLogit, PairLogitPairwise, QuerySoftMax, LambdaMart, YetiRank,
+StochasticRank) to upstream.
 
 tests/golden/ranking_corpus.npz comes from the reference's frozen ranking
 corpus (crates/cb-oracle/fixtures/ranking_corpus: 12 objects in 5 contiguous
@@ -10,7 +10,9 @@ Gradient leaves (the fixture's leaf_estimation_method); LambdaMart the NDCG
 lambda ders of a stable approx-descending sort (ranking_der.rs:482-628) with
 Newton leaves; YetiRank pairs sampled per tree and phase from TFastRng64
 query seeds (crates/cb-train/src/yetirank.rs) with separate learning-fold and
-model approximants (boosting.rs:4997-5060, 7347-7420, 8070-8200, 8787-8880).
+model approximants (boosting.rs:4997-5060, 7347-7420, 8070-8200, 8787-8880);
+StochasticRank's Monte-Carlo DCG ders with the same seeder's recalc bases
+(ranking_der.rs:640-1000, boosting.rs:5065-5100).
 PairLogitPairwise scores
 splits with the pairwise statistics and a per-candidate Cholesky solve
 (crates/cb-compute/src/pairwise_scoring.rs) and takes its leaves from the
@@ -44,6 +46,10 @@ def _fit(d, loss, borders, **kw):
     if loss == "QuerySoftMax":
         assert p["leaf_estimation_method"] == "Gradient"
         args.update(softmax_lambda=p["softmax_lambda"], softmax_beta=p["softmax_beta"])
+    if loss == "StochasticRank":
+        assert p["leaf_estimation_method"] == "Gradient"
+        args.update(srank_metric=p["srank_metric"], srank_sigma=p["srank_sigma"], srank_mu=p["srank_mu"],
+                    srank_num_estimations=p["srank_num_estimations"])
     if loss == "YetiRank":
         args.update(yeti_permutations=p["yeti_permutations"], yeti_decay=p["yeti_decay"])
     if loss == "LambdaMart":
@@ -55,7 +61,7 @@ def _fit(d, loss, borders, **kw):
 
 
 @pytest.mark.parametrize("loss", ["QueryRMSE", "PairLogit", "PairLogitPairwise", "QuerySoftMax", "LambdaMart",
-                                  "YetiRank"])
+                                  "YetiRank", "StochasticRank"])
 @pytest.mark.parametrize("border_set", ["full", "model"])
 def test_ranking_matches_upstream(loss, border_set):
     d = _load()
@@ -121,3 +127,23 @@ def test_yetirank_tree_seeder_matches_trainer_log():
     gt = d["yeti_gt_recalc_seeds"]
     ours = oracle.yeti_recalc_seeds(20260617, 5, 4, 2, gt.shape[0])
     np.testing.assert_array_equal(ours[:, [0, 2, 1]], gt)
+
+
+def test_stochasticrank_noise_matches_trainer_log():
+    # each logged draw: seed = recalc base + group index, one std_normal per
+    # document per sample, in document order
+    d = _load()
+    seeds, rows = d["srank_gt_noise_seed"], d["srank_gt_noise"]
+    streams = {}
+    for s, (sample, doc, count, noise) in zip(seeds, rows):
+        key = int(s)
+        if key not in streams:
+            streams[key] = oracle.TFastRng64(key)
+        assert int(doc) < int(count)
+        got = streams[key].std_normal()
+        assert abs(got - noise) <= 1e-12
+    # every logged stream is a derivative or leaf-value recalc base of the
+    # corpus fit (random_seed 20260617, 5 groups, 4 features, depth 2) + group
+    bases = oracle.yeti_recalc_seeds(20260617, 5, 4, 2, 5)[:, [0, 2]].ravel()
+    valid = {(int(b) + g) % 2**64 for b in bases for g in range(5)}
+    assert {int(s) for s in seeds} <= valid
