@@ -18,7 +18,9 @@ OK, DECLINED, ERR_INVALID, ERR_CUDA, ERR_OOM, ERR_NCCL, ERR_DEVICE, ERR_NO_DEVIC
 class RankParams(C.Structure):
     _fields_ = [("l2_leaf_reg", C.c_double), ("softmax_lambda", C.c_double), ("softmax_beta", C.c_double),
                 ("lambdamart_sigma", C.c_double), ("lambdamart_top", C.c_int64), ("lambdamart_norm", C.c_int32),
-                ("lambdamart_metric", C.c_int32), ("yeti_permutations", C.c_int32), ("yeti_decay", C.c_double)]
+                ("lambdamart_metric", C.c_int32), ("yeti_permutations", C.c_int32), ("yeti_decay", C.c_double),
+                ("srank_metric", C.c_int32), ("srank_num_estimations", C.c_int32), ("srank_sigma", C.c_double),
+                ("srank_mu", C.c_double)]
 
 
 class BeginArgs(C.Structure):

@@ -38,6 +38,10 @@ class FitParams:
     lambdamart_metric: str = "NDCG"
     yeti_permutations: int = 10    # YetiRank:permutations
     yeti_decay: float = 0.85       # YetiRank:decay
+    srank_metric: str = "DCG"      # StochasticRank:metric (DCG / NDCG)
+    srank_sigma: float = 1.0
+    srank_mu: float = 0.0
+    srank_num_estimations: int = 1
 
 
 @dataclass
@@ -240,8 +244,8 @@ def normalize_leaf_values(pairwise: bool, lr: float, leaf_weights, raw) -> np.nd
 def fit_ranking(float_columns: Sequence[np.ndarray], borders: Sequence[Sequence[float]], target, group_offsets,
                 params: FitParams, pairs=None, weights=None, *, staged: bool = False,
                 device: int = 0) -> RankingModel:
-    """QueryRMSE / QuerySoftMax / LambdaMart / YetiRank / PairLogit /
-    PairLogitPairwise fit (params.loss) on raw f32 columns with fixed borders:
+    """QueryRMSE / QuerySoftMax / LambdaMart / YetiRank / StochasticRank /
+    PairLogit / PairLogitPairwise fit (params.loss) on raw f32 columns with fixed borders:
     cb-train's grouped
     loop (pointwise histograms with Newton or, for QuerySoftMax, Gradient
     leaves; or pairwise scoring and Cholesky leaves) over the device's ranking
@@ -263,7 +267,9 @@ def fit_ranking(float_columns: Sequence[np.ndarray], borders: Sequence[Sequence[
                               softmax_lambda=p.softmax_lambda, softmax_beta=p.softmax_beta,
                               lambdamart_sigma=p.lambdamart_sigma, lambdamart_top=p.lambdamart_top,
                               lambdamart_norm=p.lambdamart_norm, lambdamart_metric=p.lambdamart_metric,
-                              yeti_permutations=p.yeti_permutations, yeti_decay=p.yeti_decay)
+                              yeti_permutations=p.yeti_permutations, yeti_decay=p.yeti_decay,
+                              srank_metric=p.srank_metric, srank_sigma=p.srank_sigma, srank_mu=p.srank_mu,
+                              srank_num_estimations=p.srank_num_estimations)
     if not ok:
         raise RuntimeError(f"device declined: {rt.decline_reason}")
     T, D = p.iterations, p.depth

@@ -487,7 +487,7 @@ __global__ void mc_apply_pending_kernel(int64_t n, int K, int L, double* __restr
 // ---- ranking mode (grouped losses, K = 1) ----------------------------------
 
 enum : int { kRankQueryRmse = 0, kRankPairLogit = 1, kRankPairLogitPairwise = 2, kRankQuerySoftMax = 3,
-             kRankLambdaMart = 4, kRankYetiRank = 5 };
+             kRankLambdaMart = 4, kRankYetiRank = 5, kRankStochasticRank = 6 };
 
 // Per-loss parameters of rk_der_kernel.  LambdaMart's position denominators
 // log2(2 + pos) (as log(x) * log2(e), ranking_der.rs:456-467) and each group's
@@ -743,6 +743,161 @@ __global__ void rk_newton_kernel(int L, int pairwise, int gradient, const unsign
         }
         leaf_lrv[q] = __dmul_rn(v, lr);
     }
+}
+
+// ---- StochasticRank: Monte-Carlo DCG / NDCG ders on the device -------------
+
+// Marsaglia polar standard normal over a TFastRng64 (normal.rs; the same draw
+// sequence as the host replica).
+__device__ double srk_std_normal(Rng64& r) {
+    for (;;) {
+        const double x = __dsub_rn(__dmul_rn(real1(r), 2.0), 1.0);
+        const double y = __dsub_rn(__dmul_rn(real1(r), 2.0), 1.0);
+        const double rr = __dadd_rn(__dmul_rn(x, x), __dmul_rn(y, y));
+        if (!(rr > 1.0 || rr <= 0.0)) return __dmul_rn(x, sqrt(__ddiv_rn(__dmul_rn(-2.0, log(rr)), rr)));
+    }
+}
+
+// normal_density (ranking_der.rs:640-655)
+__device__ __forceinline__ double srk_density(double x, double mean, double sigma) {
+    const double t = __ddiv_rn(__dsub_rn(x, mean), sigma);
+    const double z = __dmul_rn(t, t);
+    return __ddiv_rn(__dmul_rn(exp(__ddiv_rn(-z, 2.0)), 0.398942280401432677939946), sigma);
+}
+
+// stochastic_rank_group_der (ranking_der.rs:710-910), one thread per group:
+// group-mean centring, the Mu tie shift, num_est samples of TFastRng64(base +
+// group) noise with a stable descending sort, the DCG cumulative statistics
+// and the per-position density-weighted metric diffs, then the SFA mean
+// removal and approx-direction projection (Nu 0.01, Lambda 1).  Position
+// denominators and the NDCG ideal come from the host.  der2 = 0.
+// ws: 9 g + 3 doubles per group at ws + 9 b + 3 gi; ord: n int32.
+__global__ void rk_srank_kernel(int n_groups, const int64_t* __restrict__ goff, const double* __restrict__ approx,
+                                const double* __restrict__ target, int ndcg, double sigma_p, double mu, int num_est,
+                                uint64_t base, const double* __restrict__ den, const double* __restrict__ ideal,
+                                double* __restrict__ wsall, int32_t* __restrict__ ordall, double* __restrict__ d1,
+                                double* __restrict__ d2, McState* __restrict__ ms) {
+    const int gi = blockIdx.x * blockDim.x + threadIdx.x;
+    if (gi >= n_groups) return;
+    const int64_t b = goff[gi], cnt = goff[gi + 1] - b;
+    double* o1 = d1 + b;
+    double* o2 = d2 + b;
+    for (int64_t i = 0; i < cnt; ++i) {
+        o1[i] = 0.0;
+        o2[i] = 0.0;
+    }
+    if (cnt <= 1) return;
+    const double* tg = target + b;
+    double* ap = wsall + 9 * b + 3 * (int64_t)gi;
+    double* sh = ap + cnt;
+    double* pw = sh + cnt;
+    double* noise = pw + cnt;
+    double* sc = noise + cnt;
+    double* cs = sc + cnt;
+    double* csu = cs + cnt + 1;
+    double* csl = csu + cnt + 1;
+    double* tmp = csl + cnt + 1;
+    int32_t* ord = ordall + b;
+    const double fc = (double)cnt;
+    double acc = 0.0;
+    for (int64_t i = 0; i < cnt; ++i) acc = __dadd_rn(acc, approx[b + i]);
+    const double am = __ddiv_rn(acc, fc);
+    for (int64_t i = 0; i < cnt; ++i) ap[i] = __dsub_rn(approx[b + i], am);
+    acc = 0.0;
+    for (int64_t i = 0; i < cnt; ++i) {
+        sh[i] = __dsub_rn(ap[i], __dmul_rn(__dmul_rn(sigma_p, mu), tg[i]));
+        acc = __dadd_rn(acc, sh[i]);
+    }
+    const double avs = __ddiv_rn(acc, fc);
+    for (int64_t i = 0; i < cnt; ++i) sh[i] = __dsub_rn(sh[i], avs);
+    const double idl = ideal[gi];
+    for (int64_t p = 0; p < cnt; ++p) {
+        pw[p] = __ddiv_rn(1.0, den[p]);
+        if (ndcg && idl > DBL_EPSILON) pw[p] = __ddiv_rn(pw[p], idl);
+    }
+    Rng64 rng = Rng64::from_seed(base + (uint64_t)gi);
+    const double sigma = __dmul_rn(sigma_p, sqrt(__ddiv_rn(fc, __dsub_rn(fc, 1.0))));
+    const int ne = num_est < 1 ? 1 : num_est;
+    for (int s = 0; s < ne; ++s) {
+        double noise_sum = 0.0;
+        for (int64_t d = 0; d < cnt; ++d) {
+            noise[d] = srk_std_normal(rng);
+            sc[d] = __dadd_rn(sh[d], __dmul_rn(sigma_p, noise[d]));
+            noise_sum = __dadd_rn(noise_sum, noise[d]);
+        }
+        for (int64_t i = 0; i < cnt; ++i) ord[i] = (int32_t)i;
+        for (int64_t i = 1; i < cnt; ++i) {  // stable, descending by score
+            const int32_t key = ord[i];
+            int64_t j = i - 1;
+            while (j >= 0 && sc[ord[j]] < sc[key]) {
+                ord[j + 1] = ord[j];
+                --j;
+            }
+            ord[j + 1] = key;
+        }
+        for (int64_t p = 0; p <= cnt; ++p) {
+            cs[p] = 0.0;
+            csu[p] = 0.0;
+            csl[p] = 0.0;
+        }
+        for (int64_t p = 0; p < cnt; ++p) {  // CalcDCGCumulativeStatistics
+            const double gain = tg[ord[p]];
+            cs[p + 1] = __dadd_rn(cs[p], __dmul_rn(gain, pw[p]));
+            if (p + 1 < cnt) csl[p + 1] = __dadd_rn(csl[p], __dmul_rn(gain, pw[p + 1]));
+            if (p > 0) csu[p + 1] = __dadd_rn(csu[p], __dmul_rn(gain, pw[p - 1]));
+        }
+        csl[cnt] = csl[cnt - 1];
+        for (int64_t p = 0; p < cnt; ++p) {
+            const int32_t doc = ord[p];
+            const double score = sc[doc], a = ap[doc];
+            const double mean = __dadd_rn(a, __ddiv_rn(__dsub_rn(noise_sum, __dsub_rn(score, a)), __dsub_rn(fc, 1.0)));
+            const double gain = tg[doc];
+            double der_sum = 0.0;
+            for (int64_t np = 0; np < cnt; ++np) {
+                if (np == p) continue;
+                // calc_dcg_metric_diff (ranking_der.rs:920-965)
+                const double doc_diff = __dmul_rn(gain, __dsub_rn(pw[np], pw[p]));
+                double mid;
+                if (np < p) mid = __dsub_rn(__dsub_rn(csl[p], csl[np]), __dsub_rn(cs[p], cs[np]));
+                else mid = __dsub_rn(__dsub_rn(csu[np + 1], csu[p + 1]), __dsub_rn(cs[np + 1], cs[p + 1]));
+                const double md = __dadd_rn(doc_diff, mid);
+                double dd;
+                if (np == 0) dd = srk_density(sc[ord[0]], mean, sigma);
+                else if (np + 1 == cnt) dd = -srk_density(sc[ord[cnt - 1]], mean, sigma);
+                else if (np < p)
+                    dd = __dsub_rn(srk_density(sc[ord[np]], mean, sigma), srk_density(sc[ord[np - 1]], mean, sigma));
+                else
+                    dd = __dsub_rn(srk_density(sc[ord[np + 1]], mean, sigma), srk_density(sc[ord[np]], mean, sigma));
+                der_sum = __dadd_rn(der_sum, __dmul_rn(md, dd));
+            }
+            o1[doc] = __dadd_rn(o1[doc], __ddiv_rn(der_sum, (double)ne));
+        }
+    }
+    acc = 0.0;
+    for (int64_t i = 0; i < cnt; ++i) acc = __dadd_rn(acc, o1[i]);
+    const double avg_der = __ddiv_rn(acc, fc);
+    for (int64_t i = 0; i < cnt; ++i) o1[i] = __dsub_rn(o1[i], avg_der);
+    if (cnt > 2) {
+        acc = 0.0;
+        for (int64_t i = 0; i < cnt; ++i) acc = __dadd_rn(acc, ap[i]);
+        const double aa = __ddiv_rn(acc, fc);
+        double sq = 0.0, dot = 0.0;
+        for (int64_t i = 0; i < cnt; ++i) {
+            sh[i] = __dsub_rn(ap[i], aa);
+            sq = __dadd_rn(sq, __dmul_rn(sh[i], sh[i]));
+        }
+        for (int64_t i = 0; i < cnt; ++i) dot = __dadd_rn(dot, __dmul_rn(o1[i], sh[i]));
+        const double nr = __dadd_rn(sqrt(sq), 0.01);
+        const double norm_sqr = __dmul_rn(nr, nr);
+        if (norm_sqr > 0.0) {
+            const double k = __ddiv_rn(__dmul_rn(1.0, dot), norm_sqr);
+            for (int64_t i = 0; i < cnt; ++i) o1[i] = __dsub_rn(o1[i], __dmul_rn(k, sh[i]));
+        }
+    }
+    bool finite = true;
+    for (int64_t i = 0; i < cnt; ++i) finite &= isfinite(o1[i]);
+    if (!finite) atomicOr(&ms->err, kMcErrNonFinite);
+    (void)tmp;
 }
 
 // ---- YetiRank: per-tree pair sampling on the device --------------------------
@@ -1198,8 +1353,13 @@ struct cbgpu_multi_session {
     int64_t* d_cwoff = nullptr;
     float* d_cw = nullptr;
     double *d_yboot = nullptr, *d_lapprox = nullptr, *d_ylf_raw = nullptr, *d_ylf_lrv = nullptr;
+    // StochasticRank: metric / sigma / mu / samples and per-group scratch
+    int srank_ndcg = 1, srank_num_est = 1;
+    double srank_sigma = 1.0, srank_mu = 0.0;
+    double* d_srank_ws = nullptr;
 
     ~cbgpu_multi_session() {
+        cudaFree(d_srank_ws);
         if (st) cudaStreamSynchronize(st);
         cudaFree(d_gw);
         cudaFree(d_yseeds);
@@ -1436,6 +1596,7 @@ int cbgpu_rank_begin_raw(const cbgpu_begin_args* a, const int64_t* group_offsets
     else if (a->loss == CBGPU_LOSS_QUERYSOFTMAX) mode = kRankQuerySoftMax;
     else if (a->loss == CBGPU_LOSS_LAMBDAMART) mode = kRankLambdaMart;
     else if (a->loss == CBGPU_LOSS_YETIRANK) mode = kRankYetiRank;
+    else if (a->loss == CBGPU_LOSS_STOCHASTICRANK) mode = kRankStochasticRank;
     else return mfail(CBGPU_DECLINED, "rank_begin: loss %d is not a covered grouped loss", a->loss);
     const double l2_leaf_reg = params && params->l2_leaf_reg >= 0.0 ? params->l2_leaf_reg : a->scaled_l2;
     const double sm_lambda = params ? params->softmax_lambda : 0.01;
@@ -1458,6 +1619,14 @@ int cbgpu_rank_begin_raw(const cbgpu_begin_args* a, const int64_t* group_offsets
         if (cells > ((int64_t)1 << 31))
             return mfail(CBGPU_DECLINED, "rank_begin: YetiRank pair matrices need %lld cells (> 2^31)",
                          (long long)cells);
+    }
+    if (mode == kRankStochasticRank && params) {
+        if (params->srank_metric != 0 && params->srank_metric != 1)
+            return mfail(CBGPU_DECLINED, "rank_begin: StochasticRank covers the NDCG / DCG metrics");
+        if (!(std::isfinite(params->srank_sigma) && params->srank_sigma > 0.0) ||
+            !(std::isfinite(params->srank_mu) && params->srank_mu >= 0.0) || params->srank_num_estimations < 1)
+            return mfail(CBGPU_ERR_INVALID, "rank_begin: StochasticRank needs sigma > 0, mu >= 0 and "
+                                            "num_estimations >= 1");
     }
     if (mode == kRankLambdaMart) {
         if (params && params->lambdamart_metric != 0 && params->lambdamart_metric != 1)
@@ -1561,6 +1730,12 @@ int cbgpu_rank_begin_raw(const cbgpu_begin_args* a, const int64_t* group_offsets
         s->yeti_perms = yeti_perms;
         s->yeti_decay = yeti_decay;
         s->yeti_rng.r = Rng64::from_seed(a->rng_seed);
+        if (params) {
+            s->srank_ndcg = params->srank_metric == 0 ? 1 : 0;
+            s->srank_num_est = params->srank_num_estimations;
+            s->srank_sigma = params->srank_sigma;
+            s->srank_mu = params->srank_mu;
+        }
         rc = mdalloc(&s->d_goff, (size_t)n_groups + 1);
         if (!rc) rc = mdalloc(&s->d_cstart, (size_t)n + 1);
         if (!rc) rc = mdalloc(&s->d_closer, closer.size());
@@ -1597,7 +1772,10 @@ int cbgpu_rank_begin_raw(const cbgpu_begin_args* a, const int64_t* group_offsets
                         cudaMemset(s->d_lapprox, 0, sizeof(double) * (size_t)n) != cudaSuccess))
                 rc = mfail(CBGPU_ERR_CUDA, "rank_begin: upload failed");
         }
-        if (!rc && mode == kRankLambdaMart) {
+        if (!rc && mode == kRankStochasticRank) {
+            rc = mdalloc(&s->d_srank_ws, 9 * (size_t)n + 3 * (size_t)n_groups);
+        }
+        if (!rc && (mode == kRankLambdaMart || mode == kRankStochasticRank)) {
             int64_t maxg = 1;
             for (int g = 0; g < n_groups; ++g) maxg = std::max(maxg, group_offsets[g + 1] - group_offsets[g]);
             std::vector<double> den((size_t)maxg);
@@ -1666,18 +1844,24 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
     MCU(cudaSetDevice(s->device));
     if (!s->target_ready && s->rank_mode >= 0) {
         if (!target) return mfail(CBGPU_ERR_INVALID, "multi_grow: the first call needs the target");
-        if (s->rank_mode == kRankLambdaMart) {
-            // lambdamart_ideal_ndcg per group: the DCG of the relevance-sorted
-            // order over the top positions, summed in position order
+        if (s->rank_mode == kRankLambdaMart || s->rank_mode == kRankStochasticRank) {
+            // lambdamart_ideal_ndcg / compute_dcg_pos_weights' ideal per group:
+            // the DCG of the relevance-sorted order over the top positions,
+            // summed in position order (StochasticRank: the whole group, as
+            // relevance x (1 / denominator))
             const int G = s->n_groups;
             std::vector<double> ideal((size_t)G), ts;
             for (int g = 0; g < G; ++g) {
                 const int64_t b = s->h_goff[(size_t)g], e = s->h_goff[(size_t)g + 1], cnt = e - b;
                 ts.assign(target + b, target + e);
                 std::stable_sort(ts.begin(), ts.end(), [](double x, double y) { return x > y; });
-                const int64_t top = (s->lm_top == -1 || s->lm_top > cnt) ? cnt : s->lm_top;
+                const bool srank = s->rank_mode == kRankStochasticRank;
+                const int64_t top = (srank || s->lm_top == -1 || s->lm_top > cnt) ? cnt : s->lm_top;
                 double acc = 0.0;
-                for (int64_t p = 0; p < top; ++p) acc += ts[(size_t)p] / (std::log(2.0 + (double)p) * 1.4426950408889634);
+                for (int64_t p = 0; p < top; ++p) {
+                    const double dn = std::log(2.0 + (double)p) * 1.4426950408889634;
+                    acc += srank ? ts[(size_t)p] * (1.0 / dn) : ts[(size_t)p] / dn;
+                }
                 ideal[(size_t)g] = acc;
             }
             MCU(cudaMemcpyAsync(s->d_lmideal, ideal.data(), sizeof(double) * (size_t)G, cudaMemcpyHostToDevice, st));
@@ -1730,8 +1914,10 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
     MCU(cudaMemsetAsync(s->d_ms, 0, sizeof(McState), st));
     const unsigned g = grid_for(n);
     const bool yeti = s->rank_mode == kRankYetiRank;
+    const bool srank = s->rank_mode == kRankStochasticRank;
     const unsigned yg = (unsigned)((s->n_groups + 127) / 128);
-    if (yeti) {
+    uint64_t srank_base[2] = {0, 0};
+    if (yeti || srank) {
         // YetiRankTreeSeeder::next_tree (yetirank.rs:340-430) on the host: the
         // per-group query seeds of the three resamples of this tree
         const int G = s->n_groups;
@@ -1750,10 +1936,15 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
         }
         const uint64_t lrs = first_gen(first_gen(yr.gen()));
         const uint64_t vb = yr.gen();
-        fill(drs, s->h_yseeds);
-        fill(lrs, s->h_yseeds + G);
-        fill(vb, s->h_yseeds + 2 * (size_t)G);
-        MCU(cudaMemcpyAsync(s->d_yseeds, s->h_yseeds, sizeof(uint64_t) * 3 * (size_t)G, cudaMemcpyHostToDevice, st));
+        if (yeti) {
+            fill(drs, s->h_yseeds);
+            fill(lrs, s->h_yseeds + G);
+            fill(vb, s->h_yseeds + 2 * (size_t)G);
+            MCU(cudaMemcpyAsync(s->d_yseeds, s->h_yseeds, sizeof(uint64_t) * 3 * (size_t)G, cudaMemcpyHostToDevice,
+                                st));
+        }
+        srank_base[0] = drs;  // StochasticRank: the derivative and leaf-value bases
+        srank_base[1] = vb;
     }
     if (s->rank_mode >= 0) {
         if (s->pending)
@@ -1767,6 +1958,10 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
                                                  s->d_yboot);
         rk_yeti_der_kernel<<<yg, 128, 0, st>>>(s->n_groups, s->d_goff, s->d_lapprox, s->d_gw, s->yeti_perms,
                                               s->d_cwoff, s->d_cw, s->wd1, s->d_der2, s->d_eff, s->d_ms);
+    } else if (srank) {
+        rk_srank_kernel<<<yg, 128, 0, st>>>(s->n_groups, s->d_goff, s->approx, s->d_tgt, s->srank_ndcg, s->srank_sigma,
+                                           s->srank_mu, s->srank_num_est, srank_base[0], s->d_lmden, s->d_lmideal,
+                                           s->d_srank_ws, s->d_lmorder, s->wd1, s->d_der2, s->d_ms);
     } else if (s->rank_mode >= 0) {
         rk_der_kernel<<<(unsigned)((s->n_groups + 127) / 128), 128, 0, st>>>(
             s->n_groups, s->rank_mode, s->d_goff, s->d_cstart, s->d_closer, s->approx, s->d_tgt, s->weight,
@@ -1836,7 +2031,12 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
             rk_yeti_der_kernel<<<yg, 128, 0, st>>>(s->n_groups, s->d_goff, s->approx, s->d_gw, s->yeti_perms,
                                                   s->d_cwoff, s->d_cw, s->wd1, s->d_der2, nullptr, s->d_ms);
         }
-        const int gradient = s->rank_mode == kRankQuerySoftMax ? 1 : 0;
+        if (srank)  // the leaf-value recompute with the leaf-value base
+            rk_srank_kernel<<<yg, 128, 0, st>>>(s->n_groups, s->d_goff, s->approx, s->d_tgt, s->srank_ndcg,
+                                               s->srank_sigma, s->srank_mu, s->srank_num_est, srank_base[1],
+                                               s->d_lmden, s->d_lmideal, s->d_srank_ws, s->d_lmorder, s->wd1,
+                                               s->d_der2, s->d_ms);
+        const int gradient = (s->rank_mode == kRankQuerySoftMax || srank) ? 1 : 0;
         rk_leafsum_kernel<<<g, kMcThreads, 0, st>>>(n, L, s->wd1, s->d_der2, s->weight, s->leaf, gradient, s->sums,
                                                     s->d_ms);
         if (pairwise) {

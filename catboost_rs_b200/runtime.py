@@ -20,7 +20,7 @@ from . import _lib
 
 LOSS = {"RMSE": 0, "Rmse": 0, "Logloss": 1, "CrossEntropy": 2, "MultiClass": 3, "QueryRMSE": 4, "PairLogit": 5,
         "PairLogitPairwise": 6, "QuerySoftMax": 7,
-        "LambdaMart": 8, "YetiRank": 9}
+        "LambdaMart": 8, "YetiRank": 9, "StochasticRank": 10}
 LAMBDAMART_METRIC = {"NDCG": 0, "DCG": 1, "MRR": 2, "ERR": 3, "MAP": 4}
 SCORE = {"Cosine": 0, "L2": 1, "SolarL2": 2, "NewtonL2": 3, "NewtonCosine": 4, "LOOL2": 5, "SatL2": 6}
 BOOT = {"No": 0, "Bayesian": 1, "Bernoulli": 2, "MVS": 3, "Mvs": 3, "Poisson": 4}
@@ -322,14 +322,17 @@ class B200MultiRuntime(B200Runtime):
                           config: DeviceTrainConfig, group_offsets, pairs=None, l2_leaf_reg=None,
                           softmax_lambda=0.01, softmax_beta=1.0, lambdamart_sigma=1.0, lambdamart_top=-1,
                           lambdamart_norm=True, lambdamart_metric="NDCG", yeti_permutations=10,
-                          yeti_decay=0.85) -> bool:
+                          yeti_decay=0.85, srank_metric="DCG", srank_sigma=1.0, srank_mu=0.0,
+                          srank_num_estimations=1) -> bool:
         """The grouped families (FamilyTreeArgs::Ranking / ::Pairwise) for
-        QueryRMSE / QuerySoftMax / LambdaMart / YetiRank / PairLogit / PairLogitPairwise: group offsets
+        QueryRMSE / QuerySoftMax / LambdaMart / YetiRank / StochasticRank / PairLogit /
+        PairLogitPairwise: group offsets
         [n_groups + 1] and, for the pair losses, (winner, loser) global object
         ids; l2_leaf_reg is the unscaled l2 the pairwise scorer and leaves use
         (default scaled_l2); QuerySoftMax's lambda and beta; LambdaMart's
         sigma, top, norm and metric (NDCG / DCG); YetiRank's permutations and
-        decay (its pairs are sampled on the device); grown with
+        decay (its pairs are sampled on the device); StochasticRank's metric
+        (DCG / NDCG), sigma, mu and num_estimations; grown with
         grow_tree_on_device (family None, approx_dim 1)."""
         self.end_device_training()
         cols = [np.ascontiguousarray(c, dtype=np.float32) for c in float_columns]
@@ -350,7 +353,8 @@ class B200MultiRuntime(B200Runtime):
         rp = _lib.RankParams(-1.0 if l2_leaf_reg is None else float(l2_leaf_reg), float(softmax_lambda),
                              float(softmax_beta), float(lambdamart_sigma), int(lambdamart_top),
                              1 if lambdamart_norm else 0, LAMBDAMART_METRIC[lambdamart_metric],
-                             int(yeti_permutations), float(yeti_decay))
+                             int(yeti_permutations), float(yeti_decay), LAMBDAMART_METRIC[srank_metric],
+                             int(srank_num_estimations), float(srank_sigma), float(srank_mu))
         rc = self._L.cbgpu_rank_begin_raw(C.byref(a), _ptr(go), go.size - 1, _ptr(pw), _ptr(pl), pw.size,
                                           C.byref(rp), colptrs, _ptr(flat), _ptr(counts), C.byref(self._s))
         ok = self._finish_begin(rc, n, depth)

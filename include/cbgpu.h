@@ -51,7 +51,8 @@ typedef enum {
 typedef enum {
     CBGPU_LOSS_RMSE = 0, CBGPU_LOSS_LOGLOSS = 1, CBGPU_LOSS_CROSSENTROPY = 2, CBGPU_LOSS_MULTICLASS = 3,
     CBGPU_LOSS_QUERYRMSE = 4, CBGPU_LOSS_PAIRLOGIT = 5, CBGPU_LOSS_PAIRLOGIT_PAIRWISE = 6,
-    CBGPU_LOSS_QUERYSOFTMAX = 7, CBGPU_LOSS_LAMBDAMART = 8, CBGPU_LOSS_YETIRANK = 9
+    CBGPU_LOSS_QUERYSOFTMAX = 7, CBGPU_LOSS_LAMBDAMART = 8, CBGPU_LOSS_YETIRANK = 9,
+    CBGPU_LOSS_STOCHASTICRANK = 10
 } cbgpu_loss;
 
 /* EScoreFunction (runtime.rs:834-864); Cosine is the default. */
@@ -293,11 +294,16 @@ typedef struct {
     int32_t lambdamart_metric; /* 0 = NDCG (default), 1 = DCG; MRR / ERR / MAP decline */
     int32_t yeti_permutations; /* YetiRank permutations (default 10) */
     double yeti_decay;         /* YetiRank decay (default 0.85) */
+    int32_t srank_metric;      /* StochasticRank metric: 0 = NDCG, 1 = DCG; others decline */
+    int32_t srank_num_estimations; /* StochasticRank num_estimations (default 1) */
+    double srank_sigma;        /* StochasticRank sigma (default 1.0) */
+    double srank_mu;           /* StochasticRank mu (default 0.0) */
 } cbgpu_rank_params;
 
 /* The seam's grouped families (FamilyTreeArgs::Ranking / ::Pairwise,
  * runtime.rs:918-934) for QueryRMSE, QuerySoftMax, LambdaMart, YetiRank,
- * PairLogit and PairLogitPairwise: the reference's device session declines them
+ * StochasticRank, PairLogit and PairLogitPairwise: the reference's device
+ * session declines them
  * (crates/cb-backend/src/gpu_runtime/session.rs:1401-1444); this mode
  * reproduces cb-train's grouped CPU branch (grouped ders,
  * crates/cb-compute/src/ranking_der.rs:139-440; PairLogit's pairwise
@@ -307,6 +313,9 @@ typedef struct {
  * query seeds of YetiRankTreeSeeder (crates/cb-train/src/yetirank.rs), keeps
  * the learning-fold approximant beside the model's, and takes Newton leaves
  * (boosting.rs:7347-7420, 8070-8200, 8787-8880); explicit pairs are not used.
+ * StochasticRank draws each group's Monte-Carlo noise on the device from the
+ * same seeder's recalc bases (boosting.rs:5065-5100) and takes Gradient
+ * leaves.
  * PairLogitPairwise scores splits with the pairwise scorer
  * (crates/cb-compute/src/pairwise_scoring.rs:101-580) and takes Cholesky
  * pairwise leaves (crates/cb-train/src/pairwise_leaves.rs:51-242), both with

@@ -1,5 +1,5 @@
-"""The grouped-loss (QueryRMSE, QuerySoftMax, LambdaMart, YetiRank, PairLogit, PairLogitPairwise) device mode against
-upstream and the oracle.
+"""The grouped-loss (QueryRMSE, QuerySoftMax, LambdaMart, YetiRank, StochasticRank, PairLogit, PairLogitPairwise)
+device mode against upstream and the oracle.
 
 The device mode (csrc/multi.cu, cbgpu_rank_begin_raw) reproduces cb-train's
 grouped CPU branch: grouped ders (crates/cb-compute/src/ranking_der.rs),
@@ -35,7 +35,7 @@ def cb():
 
 
 @pytest.mark.parametrize("loss", ["QueryRMSE", "PairLogit", "PairLogitPairwise", "QuerySoftMax", "LambdaMart",
-                                  "YetiRank"])
+                                  "YetiRank", "StochasticRank"])
 def test_ranking_fixture(cb, loss):
     z = np.load(GOLDEN)
     p = json.loads(str(z[f"{loss}__params"]))
@@ -46,7 +46,9 @@ def test_ranking_fixture(cb, loss):
                       softmax_lambda=p.get("softmax_lambda", 0.01), softmax_beta=p.get("softmax_beta", 1.0),
                       lambdamart_sigma=p.get("lambdamart_sigma", 1.0), lambdamart_top=p.get("lambdamart_top", -1),
                       lambdamart_norm=p.get("lambdamart_norm", True), yeti_permutations=p.get("yeti_permutations", 10),
-                      yeti_decay=p.get("yeti_decay", 0.85))
+                      yeti_decay=p.get("yeti_decay", 0.85), srank_metric=p.get("srank_metric", "DCG"),
+                      srank_sigma=p.get("srank_sigma", 1.0), srank_mu=p.get("srank_mu", 0.0),
+                      srank_num_estimations=p.get("srank_num_estimations", 1))
     m = cb.fit_ranking([X[:, f].copy() for f in range(X.shape[1])], borders, z["y"], z["group_offsets"], fp,
                        pairs=z["pairs"], staged=True)
     np.testing.assert_array_equal(m.split_feature, z[f"{loss}__split_feature"])
@@ -157,6 +159,26 @@ def test_yetirank_matches_oracle(cb, perms, decay, weighted):
     np.testing.assert_array_equal(m.split_feature, o.split_feature)
     np.testing.assert_array_equal(m.split_bin, o.split_bin)
     assert np.max(np.abs(m.raw_leaf_values - o.raw_leaf_values)) <= TOL
+    assert np.max(np.abs(m.leaf_values - o.leaf_values)) <= TOL
+    assert np.max(np.abs(m.staged - o.staged)) <= TOL
+
+
+@pytest.mark.parametrize("metric,sigma,mu,ne", [("DCG", 1.0, 0.0, 1), ("NDCG", 0.5, 0.3, 3)])
+def test_stochasticrank_matches_oracle(cb, metric, sigma, mu, ne):
+    # per-group Monte-Carlo noise drawn on the device from the host seeder's bases
+    X, y, offsets, pairs = _ranking_data(60, 8, 71)
+    n, F = X.shape
+    borders = [oracle.select_borders(X[:, f], 48) for f in range(F)]
+    fp = cb.FitParams(loss="StochasticRank", depth=4, iterations=3, learning_rate=0.3, l2_leaf_reg=3.0,
+                      random_seed=9, boost_from_average=False, srank_metric=metric, srank_sigma=sigma, srank_mu=mu,
+                      srank_num_estimations=ne)
+    m = cb.fit_ranking([X[:, f].copy() for f in range(F)], borders, y, offsets, fp, staged=True)
+    bins = oracle.quantize(X.T.copy(), borders)
+    o = oracle.train_ranking(bins, [len(b) for b in borders], y, offsets, loss="StochasticRank", depth=4,
+                             iterations=3, learning_rate=0.3, l2_leaf_reg=3.0, random_seed=9, srank_metric=metric,
+                             srank_sigma=sigma, srank_mu=mu, srank_num_estimations=ne)
+    np.testing.assert_array_equal(m.split_feature, o.split_feature)
+    np.testing.assert_array_equal(m.split_bin, o.split_bin)
     assert np.max(np.abs(m.leaf_values - o.leaf_values)) <= TOL
     assert np.max(np.abs(m.staged - o.staged)) <= TOL
 
