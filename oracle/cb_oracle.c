@@ -474,14 +474,58 @@ typedef struct {
     int draws;        /* perturbed path (draws_active) */
     orc_rng* rng;
     double std_dev;
+    int32_t C;                /* one-hot cat features, candidates after the floats */
+    const uint8_t* cat_bins;  /* [C][n] */
 } search_ctx;
+
+/* scan_and_score_one_hot_bins_into (histogram.rs:1160-1290): per parent the
+ * totals summed over the bins as the border path does, then per present bin
+ * v the TRUE child = the bin's cell, the FALSE child = total - cell. */
+static void scan_one_hot(const double* hist, int32_t n_parent, int32_t n_bins, const uint8_t* present,
+                         int32_t score_fn, double l2, double* scores, double* work) {
+    double* tot_w = work;
+    double* tot_d = tot_w + n_parent;
+    double* ld = tot_d + n_parent;
+    double* lw = ld + 2 * n_parent;
+    for (int32_t q = 0; q < n_parent; ++q) {
+        const double* row = hist + (int64_t)q * n_bins * 2;
+        double sw = 0.0, sd = 0.0;
+        for (int32_t b = 0; b < n_bins; ++b) sw += row[2 * b + 1];
+        for (int32_t b = 0; b < n_bins; ++b) sd += row[2 * b + 0];
+        tot_w[q] = sw;
+        tot_d[q] = sd;
+    }
+    for (int32_t v = 0; v < n_bins; ++v) {
+        if (!present[v]) {
+            scores[v] = -INFINITY;
+            continue;
+        }
+        for (int32_t q = 0; q < n_parent; ++q) {
+            const double* cell = hist + ((int64_t)q * n_bins + v) * 2;
+            ld[q] = tot_d[q] - cell[0];
+            lw[q] = tot_w[q] - cell[1];
+            ld[q + n_parent] = cell[0];
+            lw[q + n_parent] = cell[1];
+        }
+        scores[v] = split_score(score_fn, ld, lw, 2 * n_parent, l2);
+    }
+}
 
 /* Returns the number of splits taken; fills feat/bin and leaf_of. */
 static int search_tree(const search_ctx* c, int32_t* feat, int32_t* sbin, int32_t* leaf_of,
                        int* err) {
     const int64_t n = c->n;
-    const int32_t F = c->F, NB = c->n_bins;
+    const int32_t F0 = c->F, C = c->C, F = c->F + c->C, NB = c->n_bins;
     *err = 0;
+    if (C > 0 && c->draws) { /* upstream rejects one-hot with draws active (tree.rs:1403-1420) */
+        *err = 2;
+        return 0;
+    }
+    /* distinct_bins_ascending (tree.rs:3606-3615): the candidates of each cat column */
+    uint8_t* present = (uint8_t*)calloc((size_t)(C > 0 ? C : 1) * (size_t)(NB > 0 ? NB : 1), 1);
+    for (int32_t k = 0; k < C; ++k)
+        for (int64_t o = 0; o < n; ++o)
+            if (c->cat_bins[(int64_t)k * n + o] < NB) present[(size_t)k * NB + c->cat_bins[(int64_t)k * n + o]] = 1;
     double** cur = (double**)calloc((size_t)F, sizeof(double*));
     double* scores_all = (double*)malloc(sizeof(double) * (size_t)F * (size_t)(NB > 0 ? NB : 1));
     for (int64_t o = 0; o < n; ++o) leaf_of[o] = 0;
@@ -500,9 +544,10 @@ static int search_tree(const search_ctx* c, int32_t* feat, int32_t* sbin, int32_
         double** next = (double**)calloc((size_t)F, sizeof(double*));
 #pragma omp parallel for schedule(dynamic, 1)
         for (int32_t f = 0; f < F; ++f) {
-            int32_t nb = c->bc[f];
+            const int cat = f >= F0;
+            int32_t nb = cat ? NB : c->bc[f];
             if (nb == 0) continue;
-            const uint8_t* col = c->bins + (int64_t)f * n;
+            const uint8_t* col = cat ? c->cat_bins + (int64_t)(f - F0) * n : c->bins + (int64_t)f * n;
             size_t cells = (size_t)n_leaves * NB * 2;
             double* hist = (double*)calloc(cells, sizeof(double));
             if (level == 0) {
@@ -547,8 +592,12 @@ static int search_tree(const search_ctx* c, int32_t* feat, int32_t* sbin, int32_
                 free(built);
             }
             double* work = (double*)malloc(sizeof(double) * (size_t)n_leaves * 8);
-            scan_and_score(hist, n_leaves, NB, nb, c->score_fn, c->l2,
-                           scores_all + (size_t)f * NB, work);
+            if (cat)
+                scan_one_hot(hist, n_leaves, NB, present + (size_t)(f - F0) * NB, c->score_fn, c->l2,
+                             scores_all + (size_t)f * NB, work);
+            else
+                scan_and_score(hist, n_leaves, NB, nb, c->score_fn, c->l2,
+                               scores_all + (size_t)f * NB, work);
             free(work);
             next[f] = hist;
         }
@@ -560,11 +609,14 @@ static int search_tree(const search_ctx* c, int32_t* feat, int32_t* sbin, int32_
         if (!c->draws) {
             /* select_best: strict > over (feature asc, border asc) (tree.rs:355-366) */
             double best = -INFINITY;
-            for (int32_t f = 0; f < F; ++f)
-                for (int32_t b = 0; b < c->bc[f]; ++b) {
+            for (int32_t f = 0; f < F; ++f) {
+                const int32_t nc = f >= F0 ? NB : c->bc[f];
+                for (int32_t b = 0; b < nc; ++b) {
+                    if (f >= F0 && !present[(size_t)(f - F0) * NB + b]) continue;
                     double s = scores_all[(size_t)f * NB + b];
                     if (s > best) { best = s; best_f = f; best_b = b; }
                 }
+            }
             if (best_f < 0) { *err = 1; break; }
         } else {
             /* perturbed selection (tree.rs:1498-1606) */
@@ -605,14 +657,22 @@ static int search_tree(const search_ctx* c, int32_t* feat, int32_t* sbin, int32_
         feat[level] = best_f;
         sbin[level] = best_b;
         taken = level + 1;
-        /* advance_leaf_only (tree.rs:1005-1016): the new split is the high bit */
-        const uint8_t* col = c->bins + (int64_t)best_f * n;
-        for (int64_t o = 0; o < n; ++o)
-            if ((int32_t)col[o] > best_b) leaf_of[o] += n_leaves;
+        /* advance_leaf_only (tree.rs:1005-1016): the new split is the high bit;
+         * a one-hot split passes on bin == value */
+        if (best_f >= F0) {
+            const uint8_t* col = c->cat_bins + (int64_t)(best_f - F0) * n;
+            for (int64_t o = 0; o < n; ++o)
+                if ((int32_t)col[o] == best_b) leaf_of[o] += n_leaves;
+        } else {
+            const uint8_t* col = c->bins + (int64_t)best_f * n;
+            for (int64_t o = 0; o < n; ++o)
+                if ((int32_t)col[o] > best_b) leaf_of[o] += n_leaves;
+        }
     }
     for (int32_t f = 0; f < F; ++f) free(cur[f]);
     free(cur);
     free(scores_all);
+    free(present);
     return taken;
 }
 
@@ -621,7 +681,7 @@ static int search_tree(const search_ctx* c, int32_t* feat, int32_t* sbin, int32_
 int orc_search_tree(int64_t n, int32_t F, int32_t n_bins, int32_t depth, int32_t score_fn, const uint8_t* bins,
                     const int32_t* border_counts, const double* g, const double* h, double l2, int32_t draws,
                     orc_rng* rng, int32_t* feat, int32_t* sbin, int32_t* leaf_of, int32_t* err) {
-    search_ctx sc = {n, F, n_bins, depth, score_fn, bins, border_counts, g, h, l2, draws, rng, 0.0};
+    search_ctx sc = {n, F, n_bins, depth, score_fn, bins, border_counts, g, h, l2, draws, rng, 0.0, 0, NULL};
     int e = 0;
     int taken = search_tree(&sc, feat, sbin, leaf_of, &e);
     *err = e;
@@ -642,6 +702,8 @@ int orc_train(const orc_train_args* a, orc_train_out* o) {
     int32_t NB = 1;
     for (int32_t f = 0; f < F; ++f)
         if (a->border_counts[f] + 1 > NB) NB = a->border_counts[f] + 1;
+    for (int64_t k = 0; k < (int64_t)a->n_cat * n; ++k)
+        if (a->cat_bins_fm[k] + 1 > NB) NB = a->cat_bins_fm[k] + 1;
     const int32_t L = 1 << a->depth;
 
     double* w = (double*)malloc(sizeof(double) * (size_t)n);
@@ -703,7 +765,7 @@ int orc_train(const orc_train_args* a, orc_train_out* o) {
             std_dev = a->random_strength * dsdz * (left / (1.0 + left));
         }
         search_ctx sc = {n, F, NB, a->depth, a->score_function, a->bins_fm, a->border_counts,
-                         sg, sh, scaled_l2, draws, &rng, std_dev};
+                         sg, sh, scaled_l2, draws, &rng, std_dev, a->n_cat, a->cat_bins_fm};
         int32_t* tf = o->split_feature + (size_t)it * a->depth;
         int32_t* tb = o->split_bin + (size_t)it * a->depth;
         for (int32_t l = 0; l < a->depth; ++l) { tf[l] = -1; tb[l] = -1; }
@@ -741,3 +803,123 @@ int orc_train(const orc_train_args* a, orc_train_out* o) {
     free(sg); free(sh); free(leaf); free(ls);
     return rc;
 }
+
+
+/* ======================================================================== */
+/* CityHash64 v1.0 (Google's published CityHash, as catboost's               */
+/* util/digest/city.cpp) and CalcCatFeatureHash -- cat_hash.rs               */
+/* ======================================================================== */
+
+static const uint64_t kCity0 = 0xc3a5c85c97cb3127ULL, kCity1 = 0xb492b66fbe98f273ULL,
+                      kCity2 = 0x9ae16a3b2f90404fULL, kCity3 = 0xc949d7c7509e6557ULL;
+
+static uint64_t city_fetch64(const char* p) {
+    uint64_t v;
+    memcpy(&v, p, 8);
+    return v;
+}
+static uint32_t city_fetch32(const char* p) {
+    uint32_t v;
+    memcpy(&v, p, 4);
+    return v;
+}
+static uint64_t city_rotate(uint64_t v, int s) { return s == 0 ? v : ((v >> s) | (v << (64 - s))); }
+static uint64_t city_rotate1(uint64_t v, int s) { return (v >> s) | (v << (64 - s)); }
+static uint64_t city_shift_mix(uint64_t v) { return v ^ (v >> 47); }
+static uint64_t city_hash16(uint64_t u, uint64_t v) {
+    const uint64_t m = 0x9ddfea08eb382d69ULL;
+    uint64_t a = (u ^ v) * m;
+    a ^= (a >> 47);
+    uint64_t b = (v ^ a) * m;
+    b ^= (b >> 47);
+    b *= m;
+    return b;
+}
+static uint64_t city_len0to16(const char* s, size_t len) {
+    if (len > 8) {
+        const uint64_t a = city_fetch64(s), b = city_fetch64(s + len - 8);
+        return city_hash16(a, city_rotate1(b + len, (int)len)) ^ b;
+    }
+    if (len >= 4) {
+        const uint64_t a = city_fetch32(s);
+        return city_hash16(len + (a << 3), city_fetch32(s + len - 4));
+    }
+    if (len > 0) {
+        const uint8_t a = (uint8_t)s[0], b = (uint8_t)s[len >> 1], c = (uint8_t)s[len - 1];
+        const uint32_t y = (uint32_t)a + ((uint32_t)b << 8);
+        const uint32_t z = (uint32_t)len + ((uint32_t)c << 2);
+        return city_shift_mix(y * kCity2 ^ z * kCity3) * kCity2;
+    }
+    return kCity2;
+}
+static uint64_t city_len17to32(const char* s, size_t len) {
+    const uint64_t a = city_fetch64(s) * kCity1, b = city_fetch64(s + 8);
+    const uint64_t c = city_fetch64(s + len - 8) * kCity2, d = city_fetch64(s + len - 16) * kCity0;
+    return city_hash16(city_rotate(a - b, 43) + city_rotate(c, 30) + d, a + city_rotate(b ^ kCity3, 20) - c + len);
+}
+typedef struct {
+    uint64_t first, second;
+} city_pair;
+static city_pair city_weak32(uint64_t w, uint64_t x, uint64_t y, uint64_t z, uint64_t a, uint64_t b) {
+    a += w;
+    b = city_rotate(b + a + z, 21);
+    const uint64_t c = a;
+    a += x;
+    a += y;
+    b += city_rotate(a, 44);
+    city_pair r = {a + z, b + c};
+    return r;
+}
+static city_pair city_weak32s(const char* s, uint64_t a, uint64_t b) {
+    return city_weak32(city_fetch64(s), city_fetch64(s + 8), city_fetch64(s + 16), city_fetch64(s + 24), a, b);
+}
+static uint64_t city_len33to64(const char* s, size_t len) {
+    uint64_t z = city_fetch64(s + 24);
+    uint64_t a = city_fetch64(s) + (len + city_fetch64(s + len - 16)) * kCity0;
+    uint64_t b = city_rotate(a + z, 52);
+    uint64_t c = city_rotate(a, 37);
+    a += city_fetch64(s + 8);
+    c += city_rotate(a, 7);
+    a += city_fetch64(s + 16);
+    const uint64_t vf = a + z, vs = b + city_rotate(a, 31) + c;
+    a = city_fetch64(s + 16) + city_fetch64(s + len - 32);
+    z = city_fetch64(s + len - 8);
+    b = city_rotate(a + z, 52);
+    c = city_rotate(a, 37);
+    a += city_fetch64(s + len - 24);
+    c += city_rotate(a, 7);
+    a += city_fetch64(s + len - 16);
+    const uint64_t wf = a + z, ws = b + city_rotate(a, 31) + c;
+    const uint64_t r = city_shift_mix((vf + ws) * kCity2 + (wf + vs) * kCity0);
+    return city_shift_mix(r * kCity0 + vs) * kCity2;
+}
+
+uint64_t orc_city_hash64(const char* s, size_t len) {
+    if (len <= 32) return len <= 16 ? city_len0to16(s, len) : city_len17to32(s, len);
+    if (len <= 64) return city_len33to64(s, len);
+    uint64_t x = city_fetch64(s + len - 40);
+    uint64_t y = city_fetch64(s + len - 16) + city_fetch64(s + len - 56);
+    uint64_t z = city_hash16(city_fetch64(s + len - 48) + len, city_fetch64(s + len - 24));
+    city_pair v = city_weak32s(s + len - 64, len, z);
+    city_pair w = city_weak32s(s + len - 32, y + kCity1, x);
+    x = x * kCity1 + city_fetch64(s);
+    len = (len - 1) & ~(size_t)63;
+    do {
+        x = city_rotate(x + y + v.first + city_fetch64(s + 8), 37) * kCity1;
+        y = city_rotate(y + v.second + city_fetch64(s + 48), 42) * kCity1;
+        x ^= w.second;
+        y += v.first + city_fetch64(s + 40);
+        z = city_rotate(z + w.first, 33) * kCity1;
+        v = city_weak32s(s, v.second * kCity1, x + w.first);
+        w = city_weak32s(s + 32, z + w.second, y + city_fetch64(s + 16));
+        const uint64_t t = z;
+        z = x;
+        x = t;
+        s += 64;
+        len -= 64;
+    } while (len != 0);
+    return city_hash16(city_hash16(v.first, w.first) + city_shift_mix(y) * kCity1 + z,
+                       city_hash16(v.second, w.second) + x);
+}
+
+uint32_t orc_cat_hash(const char* s, size_t len) { return (uint32_t)(orc_city_hash64(s, len) & 0xffffffffULL); }

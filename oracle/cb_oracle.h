@@ -130,11 +130,22 @@ typedef struct {
     uint64_t random_seed;
     int32_t boost_from_average;
     int32_t n_threads;             /* 0 = OpenMP default */
+    /* one-hot categorical features (plain search only): perfect-hash bins
+     * (first-seen order) [n_cat][n]; split candidates are bin == value */
+    int32_t n_cat;
+    const uint8_t* cat_bins_fm;
 } orc_train_args;
 
+/* CalcCatFeatureHash (crates/cb-data/src/cat_hash.rs): CityHash64 (v1.0) of the
+ * category's string form, low 32 bits. */
+uint32_t orc_cat_hash(const char* s, size_t len);
+uint64_t orc_city_hash64(const char* s, size_t len);
+
 typedef struct {
-    int32_t* split_feature;  /* [iterations * depth] (-1 past an early stop) */
-    int32_t* split_bin;      /* [iterations * depth] border index: passes iff bin > split_bin */
+    int32_t* split_feature;  /* [iterations * depth] (-1 past an early stop); >= n_features: one-hot
+                                cat feature split_feature - n_features */
+    int32_t* split_bin;      /* [iterations * depth] border index: passes iff bin > split_bin;
+                                one-hot: passes iff cat bin == split_bin */
     int32_t* tree_depth;     /* [iterations] splits actually taken */
     double* leaf_values;     /* [iterations * 2^depth] learning-rate scaled */
     double* staged;          /* [iterations * n] or NULL */

@@ -47,6 +47,7 @@ class _TrainArgs(C.Structure):
         ("subsample", C.c_double), ("bagging_temperature", C.c_float),
         ("random_strength", C.c_double), ("random_seed", C.c_uint64),
         ("boost_from_average", C.c_int32), ("n_threads", C.c_int32),
+        ("n_cat", C.c_int32), ("cat_bins_fm", C.c_void_p),
     ]
 
 
@@ -136,6 +137,10 @@ def lib():
         L.orc_train_multiclass.argtypes = [P(_MultiArgs), P(_MultiOut)]
         L.orc_train_multiclass.restype = C.c_int
         L.orc_solve_symmetric_newton.argtypes = [C.c_void_p, C.c_void_p, C.c_int32, C.c_double, C.c_void_p]
+        L.orc_cat_hash.argtypes = [C.c_char_p, C.c_size_t]
+        L.orc_cat_hash.restype = C.c_uint32
+        L.orc_city_hash64.argtypes = [C.c_char_p, C.c_size_t]
+        L.orc_city_hash64.restype = C.c_uint64
         L.orc_train_ranking.argtypes = [P(_RankArgs), P(_RankOut)]
         L.orc_train_ranking.restype = C.c_int
         L.orc_yeti_sample_pairs.argtypes = [C.c_void_p, C.c_void_p, C.c_int64, C.c_double, C.c_int32, C.c_double,
@@ -326,10 +331,13 @@ class OracleFit:
 def train(bins_fm, border_counts, target, *, loss="RMSE", depth=6, iterations=10,
           learning_rate=0.1, l2_leaf_reg=3.0, score_function="Cosine", bootstrap_type="No",
           subsample=0.66, bagging_temperature=1.0, random_strength=0.0, random_seed=0,
-          boost_from_average=True, weights=None, staged=True, n_threads=0) -> OracleFit:
-    """The reference CPU boosting loop (crates/cb-train/src/boosting.rs) on quantized bins."""
+          boost_from_average=True, weights=None, staged=True, n_threads=0, cat_bins_fm=None) -> OracleFit:
+    """The reference CPU boosting loop (crates/cb-train/src/boosting.rs) on quantized bins;
+    cat_bins_fm [C, n] adds one-hot categorical features (split_feature >= F: cat feature
+    split_feature - F, passing on bin == split_bin)."""
     bins = np.ascontiguousarray(bins_fm, dtype=np.uint8)
     F, n = bins.shape
+    cb = None if cat_bins_fm is None else np.ascontiguousarray(cat_bins_fm, dtype=np.uint8).reshape(-1, n)
     bc = np.ascontiguousarray(border_counts, dtype=np.int32)
     t = np.ascontiguousarray(target, dtype=np.float64)
     w = None if weights is None else np.ascontiguousarray(weights, dtype=np.float64)
@@ -345,7 +353,7 @@ def train(bins_fm, border_counts, target, *, loss="RMSE", depth=6, iterations=10
     args = _TrainArgs(n, F, _p(bins), _p(bc), _p(t), _p(w), LOSS[loss], depth, iterations,
                       learning_rate, l2_leaf_reg, SCORE[score_function], BOOT[bootstrap_type],
                       subsample, bagging_temperature, random_strength, random_seed,
-                      1 if boost_from_average else 0, n_threads)
+                      1 if boost_from_average else 0, n_threads, 0 if cb is None else cb.shape[0], _p(cb))
     out = _TrainOut(_p(sf), _p(sb), _p(td), _p(lv), _p(st), _p(fa), _p(bias), _p(calls))
     rc = lib().orc_train(C.byref(args), C.byref(out))
     if rc != 0:
@@ -468,3 +476,25 @@ def yeti_recalc_seeds(random_seed: int, n_groups: int, n_features: int, depth: i
     out = np.zeros((trees, 3), dtype=np.uint64)
     lib().orc_yeti_recalc_seeds(C.c_uint64(random_seed), n_groups, n_features, depth, trees, _p(out))
     return out
+
+
+def city_hash64(s: str) -> int:
+    """CityHash64 v1.0 of the UTF-8 string."""
+    b = s.encode()
+    return lib().orc_city_hash64(b, len(b))
+
+
+def cat_hash(s: str) -> int:
+    """CalcCatFeatureHash: the low 32 bits of CityHash64 of the category's string form."""
+    b = s.encode()
+    return lib().orc_cat_hash(b, len(b))
+
+
+def perfect_hash_bins(values) -> tuple:
+    """The perfect-hash bins of one categorical column: bin = first-seen order.  Returns
+    (bins [n] uint8/uint32, the distinct values in bin order)."""
+    index = {}
+    out = np.empty(len(values), dtype=np.uint32)
+    for i, v in enumerate(values):
+        out[i] = index.setdefault(v, len(index))
+    return out, list(index)

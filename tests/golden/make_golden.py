@@ -298,6 +298,58 @@ def ranking_fixtures(ref):
     return ["ranking_corpus/" + l for l in losses]
 
 
+def one_hot_fixtures(ref):
+    """Upstream one-hot categorical fixtures: the reference's CityHash vectors
+    (crates/cb-oracle/fixtures/cat_hash: CalcCatFeatureHash and its 64-bit
+    precursor per string, per-object hashes and first-seen perfect-hash bins)
+    and the two one_hot_train Logloss fits (float columns, categorical labels,
+    the model's float borders, per-tree splits -- one-hot splits by hash --,
+    leaf values and predictions)."""
+    fx = os.path.join(ref, "crates/cb-oracle/fixtures")
+    ch = json.loads(_read(os.path.join(fx, "cat_hash/config.json")))
+    keys = sorted(ch["string_to_ui32"])
+    arrays = {"hash_strings": np.array(keys),
+              "hash_ui32": np.array([ch["string_to_ui32"][k] for k in keys], dtype=np.uint64),
+              "hash_ui64": np.array([int(ch["string_to_ui64_precursor"][k]) for k in keys], dtype=np.uint64),
+              "hash_c0_order": np.array(ch["c0_first_seen_order"]),
+              "hash_c1_order": np.array(ch["c1_first_seen_order"]),
+              "hash_per_object": np.load(os.path.join(fx, "cat_hash/cat_hashes.npy")).astype(np.uint64),
+              "hash_bins": np.load(os.path.join(fx, "cat_hash/perfect_hash_bins.npy")).astype(np.int64)}
+    names = []
+    for sc in ("default_binary", "multi"):
+        d = os.path.join(fx, "one_hot_train", sc)
+        cfg = json.loads(_read(os.path.join(d, "config.json")))
+        model = json.loads(_read(os.path.join(d, "model.json")))
+        cc = json.loads(_read(os.path.join(d, "cat_cols.json")))
+        p = cfg["params"]
+        arrays[f"{sc}__X"] = np.load(os.path.join(d, "X_float.npy")).astype(np.float32)
+        arrays[f"{sc}__y"] = np.load(os.path.join(d, "y.npy")).astype(np.float64)
+        arrays[f"{sc}__cat"] = np.array(cc["columns"])
+        arrays[f"{sc}__predictions"] = np.load(os.path.join(d, "predictions.npy")).astype(np.float64)
+        ff = model["features_info"]["float_features"]
+        for f in ff:
+            arrays[f"{sc}__borders{f['feature_index']}"] = np.array(f.get("borders") or [], dtype=np.float64)
+        trees = model["oblivious_trees"]
+        kind, feat, val = [], [], []
+        for t in trees:
+            kind.append([0 if s["split_type"] == "FloatFeature" else 1 for s in t["splits"]])
+            feat.append([s.get("float_feature_index", s.get("cat_feature_index")) for s in t["splits"]])
+            val.append([s["border"] if s["split_type"] == "FloatFeature" else float(s["value"] & 0xffffffff)
+                        for s in t["splits"]])
+        arrays[f"{sc}__split_kind"] = np.array(kind, dtype=np.int32)
+        arrays[f"{sc}__split_feature"] = np.array(feat, dtype=np.int32)
+        arrays[f"{sc}__split_value"] = np.array(val, dtype=np.float64)
+        arrays[f"{sc}__leaf_values"] = np.array([t["leaf_values"] for t in trees], dtype=np.float64)
+        arrays[f"{sc}__params"] = np.array(json.dumps({
+            "depth": int(p["depth"]), "iterations": int(p["iterations"]), "learning_rate": float(p["learning_rate"]),
+            "l2_leaf_reg": float(p["l2_leaf_reg"]), "loss": p["loss_function"], "score_function": p["score_function"],
+            "leaf_estimation_method": p["leaf_estimation_method"], "one_hot_max_size": int(p["one_hot_max_size"]),
+            "n_float": len(ff)}))
+        names.append("one_hot_train/" + sc)
+    np.savez_compressed(os.path.join(OUT, "one_hot.npz"), **arrays)
+    return names
+
+
 def main():
     ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("CB_REFERENCE", "")
     if not ref or not os.path.isdir(ref):
@@ -308,6 +360,7 @@ def main():
     written = e2e_fixtures(ref)
     written.append(multiclass_fixture(ref))
     written += ranking_fixtures(ref)
+    written += one_hot_fixtures(ref)
     with open(os.path.join(OUT, "MANIFEST.json"), "w") as f:
         json.dump({"generator": "tests/golden/make_golden.py",
                    "origin": "upstream CatBoost 1.2.10 fixtures committed under the reference's "
