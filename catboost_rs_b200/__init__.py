@@ -10,6 +10,6 @@ from .runtime import (B200MultiRuntime, B200Runtime, DeviceGrownTree, DeviceTrai
                       apply_oblivious, bootstrap_weights, flatten_oblivious, histogram, nccl_unique_id,
                       select_borders)
 from .boosting import (FitParams, MultiClassModel, ObliviousModel, RankingModel, fit,  # noqa: F401
-                       fit_multiclass, fit_ranking, normalize_leaf_values, seq_sum, starting_approx)
+                       fit_multiclass, fit_ranking, normalize_leaf_values, perfect_hash_bins, seq_sum, starting_approx)
 
 __version__ = "0.1.0"

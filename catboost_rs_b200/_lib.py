@@ -45,7 +45,7 @@ EXPORTS = [
     "cbgpu_histogram", "cbgpu_bootstrap_weights", "cbgpu_nccl_unique_id", "cbgpu_version",
     "cbgpu_session_mark", "cbgpu_session_elapsed_ms", "cbgpu_histogram_noalloc",
     "cbgpu_select_borders", "cbgpu_apply_oblivious",
-    "cbgpu_multi_begin_raw", "cbgpu_multi_grow_tree", "cbgpu_multi_approx", "cbgpu_multi_end",
+    "cbgpu_multi_begin_raw", "cbgpu_multi_begin_cat_raw", "cbgpu_multi_grow_tree", "cbgpu_multi_approx", "cbgpu_multi_end",
     "cbgpu_rank_begin_raw",
 ]
 
@@ -92,6 +92,7 @@ def load(path: str = LIB_PATH):
         "cbgpu_select_borders": ([vp, i64, i32, i32, i32, i32, i32, vp, vp], C.c_int),
         "cbgpu_apply_oblivious": ([vp, i64, i32, vp, vp, vp, i32, vp, vp, f64, vp, i32, vp], C.c_int),
         "cbgpu_multi_begin_raw": ([C.POINTER(BeginArgs), i32, vp, vp, vp, C.POINTER(vp)], C.c_int),
+        "cbgpu_multi_begin_cat_raw": ([C.POINTER(BeginArgs), i32, vp, vp, vp, i32, vp, C.POINTER(vp)], C.c_int),
         "cbgpu_multi_grow_tree": ([vp, vp, vp, i64, vp, i64, vp, vp, vp, vp, vp, i32], C.c_int),
         "cbgpu_multi_approx": ([vp, vp, i64], C.c_int),
         "cbgpu_rank_begin_raw": ([C.POINTER(BeginArgs), vp, i32, vp, vp, i64, C.POINTER(RankParams), vp, vp, vp,

@@ -161,22 +161,38 @@ class MultiClassModel:
     split_bin: np.ndarray
     leaf_values: np.ndarray
     staged: Optional[np.ndarray] = None
+    cat_values: Optional[list] = None  # per one-hot feature, its categories in bin order
 
     def split_borders(self) -> np.ndarray:
-        return np.array([[self.borders[f][b] for f, b in zip(rf, rb)]
+        """Float splits' borders; NaN for one-hot splits (split_feature >= the float count)."""
+        F = len(self.borders)
+        return np.array([[self.borders[f][b] if f < F else np.nan for f, b in zip(rf, rb)]
                          for rf, rb in zip(self.split_feature, self.split_bin)])
+
+
+def perfect_hash_bins(column):
+    """The perfect-hash bins of one categorical column as the reference's quantizer assigns
+    them: bin = the category's first-seen order.  Returns (uint32 bins [n], categories in bin
+    order)."""
+    index = {}
+    out = np.empty(len(column), dtype=np.uint32)
+    for i, v in enumerate(column):
+        out[i] = index.setdefault(v, len(index))
+    return out, list(index)
 
 
 def fit_multiclass(float_columns: Sequence[np.ndarray], borders: Sequence[Sequence[float]], target_class,
                    n_classes: int, params: FitParams, weights=None, *, staged: bool = False,
-                   device: int = 0) -> MultiClassModel:
+                   device: int = 0, cat_columns=None) -> MultiClassModel:
     """MultiClass (softmax, Newton leaves) fit on raw f32 columns with fixed
     borders: cb-train's multi-output loop (boosting.rs:7400-8930 at
-    approx_dimension K) over the device's multi-output arm."""
+    approx_dimension K) over the device's multi-output arm.  cat_columns are
+    one-hot categorical features (any hashable values; bins in first-seen
+    order); they need bootstrap No, as upstream."""
     p = params
     cols = [np.ascontiguousarray(c, dtype=np.float32) for c in float_columns]
     F = len(cols)
-    n = cols[0].size if F else 0
+    n = cols[0].size if F else (len(cat_columns[0]) if cat_columns else 0)
     y = np.ascontiguousarray(target_class, dtype=np.float64)
     w = None if weights is None else np.ascontiguousarray(weights, dtype=np.float64)
     sw = seq_sum(w) if w is not None else float(n)
@@ -187,9 +203,14 @@ def fit_multiclass(float_columns: Sequence[np.ndarray], borders: Sequence[Sequen
                             bias=0.0, sample_from_host=False, bagging_temperature=p.bagging_temperature,
                             device=device)
     rt = B200MultiRuntime()
-    n_bins = max(len(b) for b in borders) + 1
+    n_bins = max([len(b) for b in borders] + [0]) + 1
+    cat_bins, cat_values = [], []
+    for col in (cat_columns or []):
+        b, v = perfect_hash_bins(col)
+        cat_bins.append(b)
+        cat_values.append(v)
     ok = rt.begin_device_training_raw("MultiClass", p.depth, True, 1, p.score_function, cols, borders, w, n, F,
-                                      n_bins, lr, scaled_l2, cfg, approx_dim=K)
+                                      n_bins, lr, scaled_l2, cfg, approx_dim=K, cat_columns=cat_bins)
     if not ok:
         raise RuntimeError(f"device declined: {rt.decline_reason}")
     T, D = p.iterations, p.depth
@@ -208,7 +229,8 @@ def fit_multiclass(float_columns: Sequence[np.ndarray], borders: Sequence[Sequen
                 st[it] = rt.resident_approx().T
     finally:
         rt.end_device_training()
-    return MultiClassModel([np.asarray(b, dtype=np.float64) for b in borders], sf, sb, lv, st)
+    return MultiClassModel([np.asarray(b, dtype=np.float64) for b in borders], sf, sb, lv, st,
+                           cat_values if cat_columns else None)
 
 
 @dataclass

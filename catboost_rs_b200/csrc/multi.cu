@@ -17,7 +17,8 @@
 //              mc_score_kernel     every (feature, border) candidate, multi-dim
 //                                  Cosine / L2 in dimension-then-leaf order
 //              mc_argmax_kernel    strict first-wins over (feature, border)
-//              mc_route_kernel     leaf |= (bin > border) << level
+//              mc_route_kernel     leaf |= (bin > border) << level (one-hot
+//                                  categorical features: bin == value)
 //   per tree   mc_leafsum_kernel   int64 per-leaf sums of w*der1 and w*der2
 //              mc_newton_kernel    the trace-regularised symmetric Newton
 //                                  solve per leaf (Cholesky), x lr
@@ -267,15 +268,21 @@ __device__ __forceinline__ double mc_avg(double s, double w, double l2) {
 // Score of candidate (f, b) over the 2P children of this level's P leaves:
 // multi_dim_split_score_into (score.rs:192-265), false children 0..P-1 then
 // true children, dimension-then-leaf order.
+// Features f >= F0 are one-hot categorical (scan_and_score_one_hot_bins_into,
+// histogram.rs:1160-1290): candidate b is present[f - F0][b], its TRUE
+// children the bin's cells (prefix(b) - prefix(b - 1)), its FALSE children the
+// parent totals minus them.
 __global__ void mc_score_kernel(int parents, int F, int NB, int K, const unsigned long long* __restrict__ pre,
                                 const int32_t* __restrict__ border_counts, const McState* __restrict__ ms,
-                                double l2, int score_fn, double* __restrict__ scores) {
+                                double l2, int score_fn, int F0, const uint8_t* __restrict__ present,
+                                double* __restrict__ scores) {
     const int64_t cand = (int64_t)F * NB;
     const int C = K + 1;
     const double inv = ldexp(1.0, -ms->hist_shift);
     for (int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < cand; k += (int64_t)gridDim.x * blockDim.x) {
         const int f = (int)(k / NB), b = (int)(k - (int64_t)f * NB);
-        if (b >= border_counts[f] || b >= NB - 1) {
+        const bool cat = f >= F0;
+        if (cat ? !present[(size_t)(f - F0) * NB + b] : (b >= border_counts[f] || b >= NB - 1)) {
             scores[k] = -INFINITY;
             continue;
         }
@@ -285,12 +292,22 @@ __global__ void mc_score_kernel(int parents, int F, int NB, int K, const unsigne
                 for (int side = 0; side < 2; ++side) {  // false children, then true children
                     for (int q = 0; q < parents; ++q) {
                         const unsigned long long* row = pre + ((size_t)q * F + f) * NB * C;
-                        const long long wp = (long long)row[(size_t)b * C + K];
+                        long long wp = (long long)row[(size_t)b * C + K];
                         const long long wt = (long long)row[(size_t)(NB - 1) * C + K];
-                        const long long sp = (long long)row[(size_t)b * C + d];
+                        long long sp = (long long)row[(size_t)b * C + d];
                         const long long st = (long long)row[(size_t)(NB - 1) * C + d];
-                        const double w = __dmul_rn((double)(side ? wt - wp : wp), inv);
-                        const double s = __dmul_rn((double)(side ? st - sp : sp), inv);
+                        double w, s;
+                        if (cat) {  // the bin's own cell: TRUE = cell, FALSE = total - cell
+                            if (b > 0) {
+                                wp -= (long long)row[(size_t)(b - 1) * C + K];
+                                sp -= (long long)row[(size_t)(b - 1) * C + d];
+                            }
+                            w = __dmul_rn((double)(side ? wp : wt - wp), inv);
+                            s = __dmul_rn((double)(side ? sp : st - sp), inv);
+                        } else {
+                            w = __dmul_rn((double)(side ? wt - wp : wp), inv);
+                            s = __dmul_rn((double)(side ? st - sp : sp), inv);
+                        }
                         const double avg = mc_avg(s, w, l2);
                         if (pass == 0) num = __dadd_rn(num, __dmul_rn(avg, s));
                         else den = __dadd_rn(den, __dmul_rn(__dmul_rn(avg, avg), w));
@@ -351,12 +368,13 @@ __global__ void __launch_bounds__(1024) mc_argmax_kernel(int64_t cand, int NB, c
 }
 
 // advance_leaf_only (tree.rs:1005-1016): the level's split is leaf bit `level`.
-__global__ void mc_route_kernel(int64_t n, int level, const uint8_t* __restrict__ bins_fm,
+__global__ void mc_route_kernel(int64_t n, int level, const uint8_t* __restrict__ bins_fm, int F0,
                                 const McState* __restrict__ ms, uint16_t* __restrict__ leaf) {
     const McSplit sp = ms->split[level];
     const uint8_t* col = bins_fm + (size_t)sp.feature * (size_t)n;
+    const bool cat = sp.feature >= F0;  // one-hot: passes on bin == value (tree.rs:1005-1016)
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
-        if ((int)col[i] > sp.bin) leaf[i] = (uint16_t)(leaf[i] | (1u << level));
+        if (cat ? (int)col[i] == sp.bin : (int)col[i] > sp.bin) leaf[i] = (uint16_t)(leaf[i] | (1u << level));
 }
 
 // Per-leaf sums of w*der1[d] (K) and w*der2 packed (pk) over ALL rows
@@ -771,7 +789,7 @@ __device__ __forceinline__ double srk_density(double x, double mean, double sigm
 // and the per-position density-weighted metric diffs, then the SFA mean
 // removal and approx-direction projection (Nu 0.01, Lambda 1).  Position
 // denominators and the NDCG ideal come from the host.  der2 = 0.
-// ws: 9 g + 3 doubles per group at ws + 9 b + 3 gi; ord: n int32.
+// ws: 9 g + 3 doubles per group at ws + 9 b + 3 gi (8 g + 3 used); ord: n int32.
 __global__ void rk_srank_kernel(int n_groups, const int64_t* __restrict__ goff, const double* __restrict__ approx,
                                 const double* __restrict__ target, int ndcg, double sigma_p, double mu, int num_est,
                                 uint64_t base, const double* __restrict__ den, const double* __restrict__ ideal,
@@ -796,7 +814,6 @@ __global__ void rk_srank_kernel(int n_groups, const int64_t* __restrict__ goff, 
     double* cs = sc + cnt;
     double* csu = cs + cnt + 1;
     double* csl = csu + cnt + 1;
-    double* tmp = csl + cnt + 1;
     int32_t* ord = ordall + b;
     const double fc = (double)cnt;
     double acc = 0.0;
@@ -897,7 +914,6 @@ __global__ void rk_srank_kernel(int n_groups, const int64_t* __restrict__ goff, 
     bool finite = true;
     for (int64_t i = 0; i < cnt; ++i) finite &= isfinite(o1[i]);
     if (!finite) atomicOr(&ms->err, kMcErrNonFinite);
-    (void)tmp;
 }
 
 // ---- YetiRank: per-tree pair sampling on the device --------------------------
@@ -1299,6 +1315,8 @@ unsigned grid_for(int64_t n, int threads = kMcThreads) {
 
 struct cbgpu_multi_session {
     int device = 0, K = 0, depth = 0, F = 0, NB = 0, score_fn = 0, boot = 0, sample_from_host = 0;
+    int F0 = 0;                    // float features; F0..F-1 are one-hot categorical
+    uint8_t* d_present = nullptr;  // [F - F0][NB] learn-set bins of each categorical feature
     float sample_rate = 1.0f, temp = 1.0f;
     double lr = 0.0, l2 = 0.0;
     int64_t n = 0;
@@ -1359,8 +1377,9 @@ struct cbgpu_multi_session {
     double* d_srank_ws = nullptr;
 
     ~cbgpu_multi_session() {
-        cudaFree(d_srank_ws);
         if (st) cudaStreamSynchronize(st);
+        cudaFree(d_srank_ws);
+        cudaFree(d_present);
         cudaFree(d_gw);
         cudaFree(d_yseeds);
         if (h_yseeds) cudaFreeHost(h_yseeds);
@@ -1434,11 +1453,13 @@ int mhalloc(T** p, size_t count) {
 }
 
 int begin_impl(const cbgpu_begin_args* a, int32_t K, const float* const* cols, const double* borders_flat,
-               const int32_t* border_counts, cbgpu_multi_session* s) {
+               const int32_t* border_counts, int32_t n_cat, const uint32_t* const* cat_cols,
+               cbgpu_multi_session* s) {
     s->device = a->device;
     s->K = K;
     s->depth = a->depth;
-    s->F = a->n_features;
+    s->F0 = a->n_features;
+    s->F = a->n_features + n_cat;
     s->score_fn = a->score_function;
     s->boot = a->bootstrap_type;
     s->sample_from_host = a->sample_from_host;
@@ -1448,16 +1469,39 @@ int begin_impl(const cbgpu_begin_args* a, int32_t K, const float* const* cols, c
     s->l2 = a->scaled_l2;
     s->n = a->n;
     s->rng.r = Rng64::from_seed(a->rng_seed);
-    s->bc.assign(border_counts, border_counts + s->F);
+    s->bc.assign(border_counts, border_counts + s->F0);
     int maxb = 0;
-    for (int f = 0; f < s->F; ++f) maxb = std::max(maxb, (int)s->bc[(size_t)f]);
+    for (int f = 0; f < s->F0; ++f) maxb = std::max(maxb, (int)s->bc[(size_t)f]);
     s->NB = maxb + 1;
+    // one-hot columns: u8 bins and the learn-set presence of each bin
+    std::vector<uint8_t> cat_u8((size_t)n_cat * (size_t)std::max<int64_t>(a->n, 0));
+    for (int c = 0; c < n_cat; ++c) {
+        uint32_t mx = 0;
+        for (int64_t i = 0; i < a->n; ++i) {
+            const uint32_t v = cat_cols[c][i];
+            if (v > 255) return mfail(CBGPU_DECLINED, "multi_begin: categorical feature %d has bin %u (> 255)", c, v);
+            mx = std::max(mx, v);
+            cat_u8[(size_t)c * a->n + i] = (uint8_t)v;
+        }
+        s->bc.push_back((int32_t)mx + 1);
+        s->NB = std::max(s->NB, (int)mx + 1);
+    }
     const int64_t n = s->n;
     const int F = s->F, C = K + 1, L = 1 << s->depth, pk = K * (K + 1) / 2;
     MCU(cudaSetDevice(s->device));
     MCU(cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking));
     MDA(s->bins_fm, (size_t)F * n);
     MDA(s->d_bc, F);
+    if (n_cat > 0) {
+        std::vector<uint8_t> present((size_t)n_cat * s->NB, 0);
+        for (int c = 0; c < n_cat; ++c)
+            for (int64_t i = 0; i < n; ++i) present[(size_t)c * s->NB + cat_u8[(size_t)c * n + i]] = 1;
+        MDA(s->d_present, present.size());
+        MCU(cudaMemcpy(s->d_present, present.data(), present.size(), cudaMemcpyHostToDevice));
+        MCU(cudaMemcpy(s->bins_fm + (size_t)s->F0 * n, cat_u8.data(), cat_u8.size(), cudaMemcpyHostToDevice));
+    } else {
+        MDA(s->d_present, 1);
+    }
     MDA(s->approx, (size_t)K * n);
     MDA(s->wd1, (size_t)K * n);
     MDA(s->q, (size_t)C * n);
@@ -1509,7 +1553,7 @@ int begin_impl(const cbgpu_begin_args* a, int32_t K, const float* const* cols, c
     MCU(cudaMemsetAsync(d_err, 0, sizeof(uint32_t), s->st));
     int64_t off = 0;
     int rc = CBGPU_OK;
-    for (int f = 0; f < F && rc == CBGPU_OK; ++f) {
+    for (int f = 0; f < s->F0 && rc == CBGPU_OK; ++f) {
         const int nb = s->bc[(size_t)f];
         cudaError_t e = cudaMemcpyAsync(d_col, cols[f], sizeof(float) * n, cudaMemcpyHostToDevice, s->st);
         if (e == cudaSuccess && nb > 0)
@@ -1533,10 +1577,24 @@ int begin_impl(const cbgpu_begin_args* a, int32_t K, const float* const* cols, c
 
 int cbgpu_multi_begin_raw(const cbgpu_begin_args* a, int32_t approx_dim, const float* const* float_columns,
                           const double* borders_flat, const int32_t* border_counts, cbgpu_multi_session** out) {
+    return cbgpu_multi_begin_cat_raw(a, approx_dim, float_columns, borders_flat, border_counts, 0, nullptr, out);
+}
+
+int cbgpu_multi_begin_cat_raw(const cbgpu_begin_args* a, int32_t approx_dim, const float* const* float_columns,
+                              const double* borders_flat, const int32_t* border_counts, int32_t n_cat,
+                              const uint32_t* const* cat_columns, cbgpu_multi_session** out) {
     if (!out) return mfail(CBGPU_ERR_INVALID, "multi_begin: out is NULL");
     *out = nullptr;
-    if (!a || !border_counts || (a->n > 0 && !float_columns))
+    if (!a || !border_counts || (a->n > 0 && a->n_features > 0 && !float_columns) || n_cat < 0 ||
+        (n_cat > 0 && a->n > 0 && !cat_columns))
         return mfail(CBGPU_ERR_INVALID, "multi_begin: bad arguments");
+    if (n_cat > 0) {
+        for (int c = 0; c < n_cat; ++c)
+            if (!cat_columns[c]) return mfail(CBGPU_ERR_INVALID, "multi_begin: categorical column %d is NULL", c);
+        // upstream rejects one-hot columns whenever draws are active (tree.rs:1403-1420)
+        if (a->bootstrap_type != CBGPU_BOOT_NO || a->sample_from_host)
+            return mfail(CBGPU_DECLINED, "multi_begin: one-hot categorical features need bootstrap No");
+    }
     // the coverage this arm accepts; everything else declines to the CPU grower
     if (a->loss != CBGPU_LOSS_MULTICLASS) return mfail(CBGPU_DECLINED, "multi_begin: loss is not MultiClass");
     if (a->grow_policy != CBGPU_GROW_SYMMETRIC || !a->boosting_type_is_plain || a->fold_count != 1)
@@ -1552,8 +1610,9 @@ int cbgpu_multi_begin_raw(const cbgpu_begin_args* a, int32_t approx_dim, const f
     if (a->depth < 1 || a->depth > kMcMaxDepth)
         return mfail(CBGPU_DECLINED, "multi_begin: depth %d outside 1..%d", a->depth, kMcMaxDepth);
     // histogram grids index row chunks in gridDim.z (at most 65535 chunks)
-    if (a->n < 1 || a->n > (int64_t)65535 * kMcChunk || a->n_features < 1)
-        return mfail(CBGPU_ERR_INVALID, "multi_begin: n must be 1..%lld and n_features >= 1",
+    if (a->n < 1 || a->n > (int64_t)65535 * kMcChunk || a->n_features < 0 || a->n_features + n_cat < 1 ||
+        a->n_features + n_cat > 65535)
+        return mfail(CBGPU_ERR_INVALID, "multi_begin: n must be 1..%lld and features 1..65535",
                      (long long)65535 * kMcChunk);
     for (int f = 0; f < a->n_features; ++f)
         if (border_counts[f] < 0 || border_counts[f] > 255)
@@ -1571,7 +1630,7 @@ int cbgpu_multi_begin_raw(const cbgpu_begin_args* a, int32_t approx_dim, const f
     if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) return mfail(CBGPU_ERR_NO_DEVICE, "no CUDA device");
     if (a->device < 0 || a->device >= ndev) return mfail(CBGPU_ERR_INVALID, "multi_begin: bad device");
     auto* s = new cbgpu_multi_session();
-    const int rc = begin_impl(a, approx_dim, float_columns, borders_flat, border_counts, s);
+    const int rc = begin_impl(a, approx_dim, float_columns, borders_flat, border_counts, n_cat, cat_columns, s);
     if (rc) {
         delete s;
         return rc;
@@ -1717,7 +1776,7 @@ int cbgpu_rank_begin_raw(const cbgpu_begin_args* a, const int64_t* group_offsets
     if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) return mfail(CBGPU_ERR_NO_DEVICE, "no CUDA device");
     if (a->device < 0 || a->device >= ndev) return mfail(CBGPU_ERR_INVALID, "rank_begin: bad device");
     auto* s = new cbgpu_multi_session();
-    int rc = begin_impl(a, 1, float_columns, borders_flat, border_counts, s);
+    int rc = begin_impl(a, 1, float_columns, borders_flat, border_counts, 0, nullptr, s);
     if (!rc) {
         s->rank_mode = mode;
         s->n_groups = n_groups;
@@ -2013,10 +2072,11 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
                                         s->d_pwscratch, s->scores);
         } else {
             mc_score_kernel<<<grid_for((int64_t)F * NB), kMcThreads, 0, st>>>(leaves, F, NB, K, s->hist, s->d_bc,
-                                                                              s->d_ms, s->l2, s->score_fn, s->scores);
+                                                                              s->d_ms, s->l2, s->score_fn, s->F0,
+                                                                              s->d_present, s->scores);
         }
         mc_argmax_kernel<<<1, 1024, 0, st>>>((int64_t)F * NB, NB, s->scores, l, s->d_ms);
-        mc_route_kernel<<<g, kMcThreads, 0, st>>>(n, l, s->bins_fm, s->d_ms, s->leaf);
+        mc_route_kernel<<<g, kMcThreads, 0, st>>>(n, l, s->bins_fm, s->F0, s->d_ms, s->leaf);
         MCU(cudaGetLastError());
     }
     if (s->rank_mode >= 0) {

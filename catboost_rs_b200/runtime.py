@@ -296,7 +296,11 @@ class B200MultiRuntime(B200Runtime):
 
     def begin_device_training_raw(self, loss, depth, boosting_type_is_plain, fold_count, score_function,
                                   float_columns, feature_borders, weight, n, n_features, n_bins,
-                                  learning_rate, scaled_l2, config: DeviceTrainConfig, approx_dim: int = 2) -> bool:
+                                  learning_rate, scaled_l2, config: DeviceTrainConfig, approx_dim: int = 2,
+                                  cat_columns=None) -> bool:
+        """The multi-output arm's begin; cat_columns are one-hot categorical
+        features as perfect-hash bins (first-seen order, uint32 per object),
+        split features n_features + c."""
         self.end_device_training()
         cols = [np.ascontiguousarray(c, dtype=np.float32) for c in float_columns]
         if len(cols) != n_features or any(c.size != n for c in cols):
@@ -308,8 +312,13 @@ class B200MultiRuntime(B200Runtime):
         colptrs = (C.c_void_p * max(1, len(cols)))(*[c.ctypes.data for c in cols])
         a = self._args(loss, depth, boosting_type_is_plain, fold_count, score_function, weight, n,
                        n_features, n_bins, learning_rate, scaled_l2, config)
-        rc = self._L.cbgpu_multi_begin_raw(C.byref(a), int(approx_dim), colptrs, _ptr(flat), _ptr(counts),
-                                           C.byref(self._s))
+        cats = [np.ascontiguousarray(c, dtype=np.uint32) for c in (cat_columns or [])]
+        if any(c.size != n for c in cats):
+            raise _lib.CbGpuError(_lib.ERR_INVALID, "LengthMismatch: cat_columns")
+        catptrs = (C.c_void_p * max(1, len(cats)))(*[c.ctypes.data for c in cats])
+        self._keep += cats
+        rc = self._L.cbgpu_multi_begin_cat_raw(C.byref(a), int(approx_dim), colptrs, _ptr(flat), _ptr(counts),
+                                               len(cats), catptrs, C.byref(self._s))
         ok = self._finish_begin(rc, n, depth)
         self.approx_dim = int(approx_dim) if ok else 0
         return ok

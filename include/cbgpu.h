@@ -268,6 +268,19 @@ CBGPU_API int cbgpu_multi_begin_raw(const cbgpu_begin_args* args, int32_t approx
                                     const float* const* float_columns, const double* borders_flat,
                                     const int32_t* border_counts, cbgpu_multi_session** out);
 
+/* cbgpu_multi_begin_raw plus one-hot categorical features (the reference's
+ * CPU grower: equality candidates on each learn-set bin after every float
+ * candidate, TRUE = the bin, crates/cb-compute/src/histogram.rs:1160-1290,
+ * crates/cb-train/src/tree.rs:1290-1380; the reference's device session
+ * declines them).  cat_columns[c] holds the n perfect-hash bins (first-seen
+ * order, <= 255) of categorical feature c; it becomes split feature
+ * n_features + c, whose split passes iff bin == split_bin.  Declines with any
+ * bootstrap, as upstream does. */
+CBGPU_API int cbgpu_multi_begin_cat_raw(const cbgpu_begin_args* args, int32_t approx_dim,
+                                        const float* const* float_columns, const double* borders_flat,
+                                        const int32_t* border_counts, int32_t n_cat,
+                                        const uint32_t* const* cat_columns, cbgpu_multi_session** out);
+
 /* grow_tree_on_device with FamilyTreeArgs::MultiOutput (runtime.rs:1629):
  *  approx_k  [K * n] DIM-major approximant (approx_k[d * n + i]) or NULL for
  *            the resident approximant (advanced by learning_rate * leaf);

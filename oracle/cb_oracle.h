@@ -175,11 +175,13 @@ typedef struct {
     float bagging_temperature;
     uint64_t random_seed;
     int32_t n_threads;
+    int32_t n_cat;                 /* one-hot cat features (plain search only) */
+    const uint8_t* cat_bins_fm;    /* [n_cat][n] first-seen perfect-hash bins */
 } orc_multi_args;
 
 typedef struct {
-    int32_t* split_feature;  /* [iterations * depth] */
-    int32_t* split_bin;      /* [iterations * depth] */
+    int32_t* split_feature;  /* [iterations * depth]; >= n_features: one-hot cat feature - n_features */
+    int32_t* split_bin;      /* [iterations * depth]; one-hot: passes iff cat bin == split_bin */
     int32_t* tree_depth;     /* [iterations] */
     double* leaf_values;     /* [iterations * 2^depth * K] LEAF-major, learning-rate scaled */
     double* staged;          /* [iterations * n * K] object-major, or NULL */

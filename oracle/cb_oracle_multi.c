@@ -184,6 +184,46 @@ static void mc_scan_and_score(const double* hist, int32_t n_parent, int32_t NB, 
     free(tot_w);
 }
 
+/* scan_and_score_one_hot_bins_into (histogram.rs:1160-1290) over C = K + 1
+ * channels: per present bin v the TRUE children are the bin's cells, the
+ * FALSE children the parent totals minus them. */
+static void mc_scan_one_hot(const double* hist, int32_t n_parent, int32_t NB, int32_t K, const uint8_t* present,
+                            int32_t score_fn, double l2, double* scores) {
+    const int32_t C = K + 1, nl = 2 * n_parent;
+    double* tot_w = (double*)calloc((size_t)n_parent * (1 + K) + (size_t)nl * (K + 1), sizeof(double));
+    double* tot_d = tot_w + n_parent;              /* [parent][K] */
+    double* ld = tot_d + (size_t)n_parent * K;     /* [K][nl] */
+    double* lw = ld + (size_t)K * nl;              /* [nl] */
+    for (int32_t q = 0; q < n_parent; ++q) {
+        const double* row = hist + (size_t)q * NB * C;
+        double s = 0.0;
+        for (int32_t b = 0; b < NB; ++b) s += row[(size_t)b * C + K];
+        tot_w[q] = s;
+        for (int32_t d = 0; d < K; ++d) {
+            double sd = 0.0;
+            for (int32_t b = 0; b < NB; ++b) sd += row[(size_t)b * C + d];
+            tot_d[(size_t)q * K + d] = sd;
+        }
+    }
+    for (int32_t v = 0; v < NB; ++v) {
+        if (!present[v]) {
+            scores[v] = -INFINITY;
+            continue;
+        }
+        for (int32_t q = 0; q < n_parent; ++q) {
+            const double* cell = hist + ((size_t)q * NB + v) * C;
+            lw[q] = tot_w[q] - cell[K];
+            lw[q + n_parent] = cell[K];
+            for (int32_t d = 0; d < K; ++d) {
+                ld[(size_t)d * nl + q] = tot_d[(size_t)q * K + d] - cell[d];
+                ld[(size_t)d * nl + q + n_parent] = cell[d];
+            }
+        }
+        scores[v] = mc_split_score(score_fn, ld, lw, K, nl, l2);
+    }
+    free(tot_w);
+}
+
 typedef struct {
     int64_t n;
     int32_t F, NB, K, depth, score_fn;
@@ -194,14 +234,24 @@ typedef struct {
     double l2;
     int draws;
     orc_rng* rng;
+    int32_t C;                /* one-hot cat features, candidates after the floats */
+    const uint8_t* cat_bins;  /* [C][n] */
 } mc_ctx;
 
 /* the greedy oblivious search (tree.rs:704-1131, 1403-1606 at std_dev 0) over
  * K + 1 channels.  Returns the splits taken. */
 static int mc_search(const mc_ctx* c, int32_t* feat, int32_t* sbin, int32_t* leaf_of, int* err) {
     const int64_t n = c->n;
-    const int32_t F = c->F, NB = c->NB, K = c->K, C = K + 1;
+    const int32_t F0 = c->F, F = c->F + c->C, NB = c->NB, K = c->K, C = K + 1;
     *err = 0;
+    if (c->C > 0 && c->draws) { /* upstream rejects one-hot with draws active (tree.rs:1403-1420) */
+        *err = 2;
+        return 0;
+    }
+    uint8_t* present = (uint8_t*)calloc((size_t)(c->C > 0 ? c->C : 1) * (size_t)NB, 1);
+    for (int32_t k = 0; k < c->C; ++k)
+        for (int64_t o = 0; o < n; ++o)
+            if (c->cat_bins[(int64_t)k * n + o] < NB) present[(size_t)k * NB + c->cat_bins[(int64_t)k * n + o]] = 1;
     double** cur = (double**)calloc((size_t)F, sizeof(double*));
     double* scores_all = (double*)malloc(sizeof(double) * (size_t)F * (size_t)NB);
     for (int64_t o = 0; o < n; ++o) leaf_of[o] = 0;
@@ -218,9 +268,10 @@ static int mc_search(const mc_ctx* c, int32_t* feat, int32_t* sbin, int32_t* lea
         double** next = (double**)calloc((size_t)F, sizeof(double*));
 #pragma omp parallel for schedule(dynamic, 1)
         for (int32_t f = 0; f < F; ++f) {
-            int32_t nb = c->bc[f];
+            const int cat = f >= F0;
+            int32_t nb = cat ? NB : c->bc[f];
             if (nb == 0) continue;
-            const uint8_t* col = c->bins + (int64_t)f * n;
+            const uint8_t* col = cat ? c->cat_bins + (int64_t)(f - F0) * n : c->bins + (int64_t)f * n;
             size_t pc = (size_t)NB * C;
             double* hist = (double*)calloc((size_t)n_leaves * pc, sizeof(double));
             if (level == 0) {
@@ -259,7 +310,11 @@ static int mc_search(const mc_ctx* c, int32_t* feat, int32_t* sbin, int32_t* lea
                 }
                 free(built);
             }
-            mc_scan_and_score(hist, n_leaves, NB, K, nb, c->score_fn, c->l2, scores_all + (size_t)f * NB);
+            if (cat)
+                mc_scan_one_hot(hist, n_leaves, NB, K, present + (size_t)(f - F0) * NB, c->score_fn, c->l2,
+                                scores_all + (size_t)f * NB);
+            else
+                mc_scan_and_score(hist, n_leaves, NB, K, nb, c->score_fn, c->l2, scores_all + (size_t)f * NB);
             next[f] = hist;
         }
         for (int32_t f = 0; f < F; ++f) free(cur[f]);
@@ -268,11 +323,14 @@ static int mc_search(const mc_ctx* c, int32_t* feat, int32_t* sbin, int32_t* lea
         int32_t best_f = -1, best_b = -1;
         if (!c->draws) {
             double best = -INFINITY;
-            for (int32_t f = 0; f < F; ++f)
-                for (int32_t b = 0; b < c->bc[f]; ++b) {
+            for (int32_t f = 0; f < F; ++f) {
+                const int32_t nc = f >= F0 ? NB : c->bc[f];
+                for (int32_t b = 0; b < nc; ++b) {
+                    if (f >= F0 && !present[(size_t)(f - F0) * NB + b]) continue;
                     double s = scores_all[(size_t)f * NB + b];
                     if (s > best) { best = s; best_f = f; best_b = b; }
                 }
+            }
             if (best_f < 0) { *err = 1; break; }
         } else {
             /* perturbed selection at std_dev 0 (tree.rs:1498-1606) */
@@ -298,13 +356,20 @@ static int mc_search(const mc_ctx* c, int32_t* feat, int32_t* sbin, int32_t* lea
         feat[level] = best_f;
         sbin[level] = best_b;
         taken = level + 1;
-        const uint8_t* col = c->bins + (int64_t)best_f * n;
-        for (int64_t o = 0; o < n; ++o)
-            if ((int32_t)col[o] > best_b) leaf_of[o] += n_leaves;
+        if (best_f >= F0) { /* one-hot: passes on bin == value */
+            const uint8_t* col = c->cat_bins + (int64_t)(best_f - F0) * n;
+            for (int64_t o = 0; o < n; ++o)
+                if ((int32_t)col[o] == best_b) leaf_of[o] += n_leaves;
+        } else {
+            const uint8_t* col = c->bins + (int64_t)best_f * n;
+            for (int64_t o = 0; o < n; ++o)
+                if ((int32_t)col[o] > best_b) leaf_of[o] += n_leaves;
+        }
     }
     for (int32_t f = 0; f < F; ++f) free(cur[f]);
     free(cur);
     free(scores_all);
+    free(present);
     return taken;
 }
 
@@ -319,6 +384,8 @@ int orc_train_multiclass(const orc_multi_args* a, orc_multi_out* o) {
     int32_t NB = 1;
     for (int32_t f = 0; f < F; ++f)
         if (a->border_counts[f] + 1 > NB) NB = a->border_counts[f] + 1;
+    for (int64_t k = 0; k < (int64_t)a->n_cat * n; ++k)
+        if (a->cat_bins_fm[k] + 1 > NB) NB = a->cat_bins_fm[k] + 1;
     double* w = (double*)malloc(sizeof(double) * (size_t)(n > 0 ? n : 1));
     for (int64_t i = 0; i < n; ++i) w[i] = a->weights ? a->weights[i] : 1.0;
     double sum_w = orc_sum_f64(w, n);
@@ -374,7 +441,8 @@ int orc_train_multiclass(const orc_multi_args* a, orc_multi_out* o) {
                 sg[(size_t)d * n + i] = ctl[i] ? wd1[(size_t)d * n + i] * sw[i] : 0.0;
             sh[i] = ctl[i] ? w[i] * sw[i] : 0.0;
         }
-        mc_ctx c = {n, F, NB, K, D, a->score_function, a->bins_fm, a->border_counts, sg, sh, scaled_l2, draws, &rng};
+        mc_ctx c = {n, F, NB, K, D, a->score_function, a->bins_fm, a->border_counts, sg, sh, scaled_l2, draws, &rng,
+                    a->n_cat, a->cat_bins_fm};
         int32_t* tf = o->split_feature + (size_t)it * D;
         int32_t* tb = o->split_bin + (size_t)it * D;
         for (int32_t l = 0; l < D; ++l) { tf[l] = -1; tb[l] = -1; }

@@ -65,7 +65,7 @@ class _MultiArgs(C.Structure):
         ("n_classes", C.c_int32), ("depth", C.c_int32), ("iterations", C.c_int32),
         ("learning_rate", C.c_double), ("l2_leaf_reg", C.c_double), ("score_function", C.c_int32),
         ("bootstrap_type", C.c_int32), ("subsample", C.c_double), ("bagging_temperature", C.c_float),
-        ("random_seed", C.c_uint64), ("n_threads", C.c_int32),
+        ("random_seed", C.c_uint64), ("n_threads", C.c_int32), ("n_cat", C.c_int32), ("cat_bins_fm", C.c_void_p),
     ]
 
 
@@ -374,10 +374,12 @@ class OracleMultiFit:
 def train_multiclass(bins_fm, border_counts, target_class, n_classes, *, depth=6, iterations=10,
                      learning_rate=0.1, l2_leaf_reg=3.0, score_function="Cosine", bootstrap_type="No",
                      subsample=0.66, bagging_temperature=1.0, random_seed=0, weights=None, staged=True,
-                     n_threads=0) -> OracleMultiFit:
-    """The reference's MultiClass (softmax, Newton leaves) CPU loop on quantized bins."""
+                     n_threads=0, cat_bins_fm=None) -> OracleMultiFit:
+    """The reference's MultiClass (softmax, Newton leaves) CPU loop on quantized bins;
+    cat_bins_fm [C, n] adds one-hot categorical features (split_feature >= F)."""
     bins = np.ascontiguousarray(bins_fm, dtype=np.uint8)
     F, n = bins.shape
+    cb = None if cat_bins_fm is None else np.ascontiguousarray(cat_bins_fm, dtype=np.uint8).reshape(-1, n)
     K = int(n_classes)
     bc = np.ascontiguousarray(border_counts, dtype=np.int32)
     y = np.ascontiguousarray(target_class, dtype=np.int32)
@@ -391,7 +393,7 @@ def train_multiclass(bins_fm, border_counts, target_class, n_classes, *, depth=6
     fa = np.empty((n, K), dtype=np.float64)
     args = _MultiArgs(n, F, _p(bins), _p(bc), _p(y), _p(w), K, depth, iterations, learning_rate, l2_leaf_reg,
                       SCORE[score_function], BOOT[bootstrap_type], subsample, bagging_temperature, random_seed,
-                      n_threads)
+                      n_threads, 0 if cb is None else cb.shape[0], _p(cb))
     out = _MultiOut(_p(sf), _p(sb), _p(td), _p(lv), _p(st), _p(fa))
     rc = lib().orc_train_multiclass(C.byref(args), C.byref(out))
     if rc != 0:

@@ -90,6 +90,57 @@ def test_multiclass_matches_oracle(cb, case):
     assert np.max(np.abs(m.staged - o.staged)) <= TOL
 
 
+def _zipf_cats(rs, n, cards):
+    # Zipf-distributed categorical ints (config 3's shape), as strings
+    cols = []
+    for card in cards:
+        p = 1.0 / np.arange(1, card + 1) ** 1.2
+        cols.append([str(v) for v in rs.choice(card, size=n, p=p / p.sum())])
+    return cols
+
+
+@pytest.mark.parametrize("score,depth", [("Cosine", 5), ("L2", 4)])
+def test_multiclass_one_hot_matches_oracle(cb, score, depth):
+    # one-hot categorical features: equality candidates after the floats,
+    # first-seen perfect-hash bins, bootstrap No (upstream rejects draws)
+    rs = np.random.RandomState(31 + depth)
+    n, F, K = 20000, 6, 5
+    X = rs.standard_normal((n, F)).astype(np.float32)
+    cats = _zipf_cats(rs, n, [5, 17, 60, 200])
+    codes = np.array([[int(v) for v in c] for c in cats])
+    lin = X[:, :3] @ rs.standard_normal((3, K)) + 3.0 * np.eye(K)[codes[0] % K] + 1.5 * np.eye(K)[codes[2] % K]
+    cls = np.argmax(lin + rs.gumbel(size=(n, K)), axis=1).astype(np.int32)
+    borders = [oracle.select_borders(X[:, f], 32) for f in range(F)]
+    fp = _fp(cb, depth=depth, iterations=4, score_function=score)
+    m = cb.fit_multiclass([X[:, f].copy() for f in range(F)], borders, cls, K, fp, staged=True, cat_columns=cats)
+    bins = oracle.quantize(X.T.copy(), borders)
+    cat_bins = np.array([oracle.perfect_hash_bins(c)[0] for c in cats])
+    o = oracle.train_multiclass(bins, [len(b) for b in borders], cls, K, depth=depth, iterations=4,
+                                learning_rate=fp.learning_rate, l2_leaf_reg=fp.l2_leaf_reg, score_function=score,
+                                cat_bins_fm=cat_bins)
+    np.testing.assert_array_equal(m.split_feature, o.split_feature)
+    np.testing.assert_array_equal(m.split_bin, o.split_bin)
+    assert (m.split_feature >= F).any()  # one-hot splits were taken
+    assert np.isnan(m.split_borders()[m.split_feature >= F]).all()
+    assert np.max(np.abs(m.leaf_values - o.leaf_values)) <= TOL
+    assert np.max(np.abs(m.staged - o.staged)) <= TOL
+
+
+def test_multiclass_one_hot_declines_bootstrap(cb):
+    rs = np.random.RandomState(3)
+    n, F, K = 2000, 2, 3
+    X = rs.standard_normal((n, F)).astype(np.float32)
+    cats = _zipf_cats(rs, n, [5])
+    cls = rs.randint(0, K, n).astype(np.int32)
+    borders = [oracle.select_borders(X[:, f], 16) for f in range(F)]
+    with pytest.raises(RuntimeError, match="bootstrap No"):
+        cb.fit_multiclass([X[:, f].copy() for f in range(F)], borders, cls, K,
+                          _fp(cb, bootstrap_type="Bernoulli", iterations=1), cat_columns=cats)
+    with pytest.raises(RuntimeError, match="> 255"):  # more than 256 categories
+        cb.fit_multiclass([X[:, f].copy() for f in range(F)], borders, cls, K, _fp(cb, iterations=1),
+                          cat_columns=[[str(i % 300) for i in range(n)]])
+
+
 def test_multiclass_host_sample_and_run_twice(cb):
     rs = np.random.RandomState(2)
     n, F, K = 8000, 6, 3

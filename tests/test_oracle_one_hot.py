@@ -119,3 +119,24 @@ def test_one_hot_rejected_with_draws():
     with pytest.raises(RuntimeError):
         oracle.train(bins, [1], d[f"{sc}__y"], loss="Logloss", depth=2, iterations=1, bootstrap_type="Bernoulli",
                      cat_bins_fm=cat)
+
+
+def test_multiclass_one_hot_binary_column_equals_float_encoding():
+    # on a two-category column the equality candidates {== bin 0, == bin 1}
+    # induce the partitions of the float border between the bins, children
+    # swapped for == 0: the same trees up to that leaf bit, the same fit
+    rs = np.random.RandomState(4)
+    n, K = 3000, 3
+    X = rs.standard_normal((n, 2)).astype(np.float32)
+    c = rs.randint(0, 2, n)
+    cls = np.argmax(np.c_[X, c] @ rs.standard_normal((3, K)) + rs.gumbel(size=(n, K)), axis=1).astype(np.int32)
+    borders = [oracle.select_borders(X[:, f], 16) for f in range(2)]
+    bins = oracle.quantize(X.T.copy(), borders)
+    cat_bins, seen = oracle.perfect_hash_bins(list(c))
+    as_float = np.vstack([bins, cat_bins.astype(np.uint8)])
+    a = oracle.train_multiclass(bins, [len(b) for b in borders], cls, K, depth=3, iterations=3,
+                                cat_bins_fm=cat_bins[None, :])
+    b = oracle.train_multiclass(as_float, [len(b) for b in borders] + [1], cls, K, depth=3, iterations=3)
+    assert (a.split_feature == 2).any()
+    np.testing.assert_array_equal(a.split_feature, b.split_feature)
+    np.testing.assert_allclose(a.final_approx, b.final_approx, rtol=0, atol=1e-12)
