@@ -13,3 +13,5 @@ from .boosting import (FitParams, MultiClassModel, ObliviousModel, RankingModel,
                        fit_multiclass, fit_ranking, normalize_leaf_values, perfect_hash_bins, seq_sum, starting_approx)
 
 __version__ = "0.1.0"
+from . import model_json  # noqa: F401,E402
+from .model_json import from_json, load_json, save_json, to_json  # noqa: F401,E402

@@ -55,6 +55,7 @@ class ObliviousModel:
     bias: float
     staged: Optional[np.ndarray] = None
     stage_timing: list = field(default_factory=list)
+    leaf_weights: Optional[np.ndarray] = None  # [T, 2^depth] when known (model.json)
 
     def split_borders(self) -> np.ndarray:
         return np.array([[self.borders[f][b] for f, b in zip(rf, rb)]
@@ -162,6 +163,7 @@ class MultiClassModel:
     leaf_values: np.ndarray
     staged: Optional[np.ndarray] = None
     cat_values: Optional[list] = None  # per one-hot feature, its categories in bin order
+    leaf_weights: Optional[np.ndarray] = None  # [T, 2^depth] when known (model.json)
 
     def split_borders(self) -> np.ndarray:
         """Float splits' borders; NaN for one-hot splits (split_feature >= the float count)."""

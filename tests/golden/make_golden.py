@@ -350,6 +350,19 @@ def one_hot_fixtures(ref):
     return names
 
 
+def model_json_fixtures(ref):
+    """Upstream model.json documents (the reference's JSON model format,
+    crates/cb-model/src/json.rs) of five fixtures, as text: the regression and
+    binary skeletons, both NaN modes, and the 3-class softmax model."""
+    fx = os.path.join(ref, "crates/cb-oracle/fixtures")
+    docs = {"regression_skeleton": "regression_skeleton/model.json", "binclf_skeleton": "binclf_skeleton/model.json",
+            "nan_mode_Max": "nan_mode/model_Max.json", "nan_mode_Min": "nan_mode/model_Min.json",
+            "multiclass_softmax": "multiclass_softmax/model.json"}
+    arrays = {k: np.array(json.dumps(json.loads(_read(os.path.join(fx, v))))) for k, v in docs.items()}
+    np.savez_compressed(os.path.join(OUT, "model_json.npz"), **arrays)
+    return ["model_json/" + k for k in docs]
+
+
 def main():
     ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("CB_REFERENCE", "")
     if not ref or not os.path.isdir(ref):
@@ -361,6 +374,7 @@ def main():
     written.append(multiclass_fixture(ref))
     written += ranking_fixtures(ref)
     written += one_hot_fixtures(ref)
+    written += model_json_fixtures(ref)
     with open(os.path.join(OUT, "MANIFEST.json"), "w") as f:
         json.dump({"generator": "tests/golden/make_golden.py",
                    "origin": "upstream CatBoost 1.2.10 fixtures committed under the reference's "

@@ -6,6 +6,9 @@ apply.rs:150-173, 374-410) over the CSR lowering of flatten_oblivious_f64
 bit for bit (same comparisons, same tree-order sum), and through it upstream
 CatBoost 1.2.10's predictions at the reference's 1e-5 bar.
 """
+import json
+import os
+
 import numpy as np
 import pytest
 
@@ -133,3 +136,14 @@ def test_fit_then_predict(cb):
     o = oracle.apply_oblivious(X.T.copy(), oracle.flatten_oblivious(m.split_feature, m.split_borders(),
                                                                       m.leaf_values), m.bias)
     np.testing.assert_array_equal(pred, o)
+
+
+@pytest.mark.parametrize("name", ["regression_skeleton", "binclf_skeleton", "nan_mode_Max", "nan_mode_Min"])
+def test_model_json_predict_on_device(cb, name):
+    # an upstream model.json read by the package's reader and applied on the device
+    z = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "model_json.npz"))
+    m = cb.from_json(json.loads(str(z[name])))
+    sc = load_scenario(name)
+    X, want = (sc["X_eval"], sc["preds_eval"]) if name.startswith("nan_mode") else (sc["X"], sc["staged"][-1])
+    got = m.predict(X)
+    assert np.max(np.abs(got - want)) <= 1e-5
