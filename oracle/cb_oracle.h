@@ -201,7 +201,8 @@ void orc_solve_symmetric_newton(const double* sum_der, const double* sum_der2_pa
 
 /* ---- grouped (ranking) losses, pointwise histograms -------------------- */
 enum { ORC_RANK_QUERYRMSE = 0, ORC_RANK_PAIRLOGIT = 1, ORC_RANK_PAIRLOGIT_PAIRWISE = 2, ORC_RANK_QUERYSOFTMAX = 3,
-       ORC_RANK_LAMBDAMART = 4, ORC_RANK_YETIRANK = 5, ORC_RANK_STOCHASTICRANK = 6 };
+       ORC_RANK_LAMBDAMART = 4, ORC_RANK_YETIRANK = 5, ORC_RANK_STOCHASTICRANK = 6,
+       ORC_RANK_YETIRANK_PAIRWISE = 7 };
 
 /* The greedy oblivious search of the scalar loop, exported for the grouped
  * loop: returns the splits taken; leaf_of gets the final leaf ids. */

@@ -400,8 +400,10 @@ void orc_yeti_recalc_seeds(uint64_t random_seed, int32_t n_groups, int32_t n_fea
  * (calc_pairwise_weights, boosting.rs:1761-1780), winner-ascending,
  * loser-ascending. */
 static void yeti_phase_ders(const orc_rank_args* a, const double* ap, const double* gw, const uint64_t* seeds,
-                            double* cwbuf, double* d1, double* d2, double* eff) {
+                            double* cwbuf, double* d1, double* d2, double* eff, int64_t* pw_out, int64_t* pl_out,
+                            double* pwt_out, int64_t* n_out) {
     const int64_t n = a->n;
+    if (n_out) *n_out = 0;
     for (int64_t i = 0; i < n; ++i) {
         d1[i] = 0.0;
         d2[i] = 0.0;
@@ -425,12 +427,23 @@ static void yeti_phase_ders(const orc_rank_args* a, const double* ap, const doub
                     eff[b + wl] += cw;
                     eff[b + ll] += cw;
                 }
+                if (n_out) { /* flatten_global_pairs order (tree.rs:3747-3760) */
+                    pw_out[*n_out] = b + wl;
+                    pl_out[*n_out] = b + ll;
+                    pwt_out[*n_out] = cw;
+                    ++*n_out;
+                }
             }
             d1[b + wl] += wd;
             d2[b + wl] += wd2;
         }
     }
 }
+
+static int pairwise_search(const orc_rank_args* a, const double* der1, const int64_t* pw, const int64_t* pl,
+                           const double* pwt, int64_t n_pairs, int32_t* feat, int32_t* sbin, int32_t* leaf_of);
+static void pairwise_leaf_deltas(const int64_t* pw, const int64_t* pl, const double* pwt, int64_t n_pairs,
+                                 const int32_t* leaf, const double* d1, int64_t n, int32_t nl, double l2, double* lv);
 
 /* Newton deltas over unit leaf weights (ordered per-leaf sums) */
 static void newton_unit(const double* d1, const double* d2, const int32_t* leaf, int64_t n, int32_t nl, double l2,
@@ -452,8 +465,12 @@ static void newton_unit(const double* d1, const double* d2, const int32_t* leaf,
  * and the histogram's pairwise weights from pairs sampled off the learning-fold
  * approximant; the stored leaves (Newton, unit weights, pairwise centring,
  * x lr) from pairs sampled off the model approximant; the learning-fold
- * approximant advanced by its own resample's Newton deltas x lr. */
+ * approximant advanced by its own resample's Newton deltas x lr.
+ * YetiRankPairwise scores the splits with the pairwise scorer over the
+ * sampled, weighted pairs and takes Cholesky pairwise leaves (raw l2) for both
+ * the stored leaves and the learning fold (boosting.rs:8270-8300, 8840-8860). */
 static int train_yetirank(const orc_rank_args* a, orc_rank_out* o, int32_t NB) {
+    const int pairwise = a->loss == ORC_RANK_YETIRANK_PAIRWISE;
     const int64_t n = a->n;
     const int32_t F = a->n_features, D = a->depth, L = 1 << D, G = a->n_groups;
     double* w = (double*)calloc((size_t)n + 1, sizeof(double));
@@ -479,6 +496,15 @@ static int train_yetirank(const orc_rank_args* a, orc_rank_out* o, int32_t NB) {
     double* lv = (double*)malloc(sizeof(double) * L);
     double* lw = (double*)malloc(sizeof(double) * L);
     uint64_t* seeds = (uint64_t*)malloc(sizeof(uint64_t) * 3 * (size_t)(G > 0 ? G : 1));
+    int64_t cells = 1, n_flat = 0;
+    for (int32_t gi = 0; gi < G; ++gi) {
+        const int64_t g = a->group_offsets[gi + 1] - a->group_offsets[gi];
+        cells += g * g;
+    }
+    int64_t* fw = pairwise ? (int64_t*)malloc(sizeof(int64_t) * (size_t)cells) : NULL;
+    int64_t* fl = pairwise ? (int64_t*)malloc(sizeof(int64_t) * (size_t)cells) : NULL;
+    double* fwt = pairwise ? (double*)malloc(sizeof(double) * (size_t)cells) : NULL;
+    int64_t* nf = pairwise ? &n_flat : NULL;
     uint64_t* sd = seeds;
     uint64_t* sl = seeds + G;
     uint64_t* sv = seeds + 2 * G;
@@ -489,24 +515,26 @@ static int train_yetirank(const orc_rank_args* a, orc_rank_out* o, int32_t NB) {
     for (int32_t it = 0; it < a->iterations; ++it) {
         yeti_next_tree(&seeder, G, F, D, sd, sl, sv, NULL);
         /* gradient / split: the learning fold */
-        yeti_phase_ders(a, lapprox, gw, sd, cwbuf, d1, d2, eff);
+        yeti_phase_ders(a, lapprox, gw, sd, cwbuf, d1, d2, eff, fw, fl, fwt, nf);
         int32_t* tf = o->split_feature + (size_t)it * D;
         int32_t* tb = o->split_bin + (size_t)it * D;
         int32_t err = 0;
-        const int taken = orc_search_tree(n, F, NB, D, a->score_function, a->bins_fm, a->border_counts, d1, eff,
-                                          scaled_l2, 0, &unused, tf, tb, leaf, &err);
-        if (err) {
+        const int taken = pairwise ? pairwise_search(a, d1, fw, fl, fwt, n_flat, tf, tb, leaf)
+                                   : orc_search_tree(n, F, NB, D, a->score_function, a->bins_fm, a->border_counts,
+                                                     d1, eff, scaled_l2, 0, &unused, tf, tb, leaf, &err);
+        if (err || taken < 0) {
             rc = -3;
             break;
         }
         const int32_t nl = 1 << taken;
         /* stored leaves: the model approximant's resample */
-        yeti_phase_ders(a, approx, gw, sv, cwbuf, d1, d2, NULL);
+        yeti_phase_ders(a, approx, gw, sv, cwbuf, d1, d2, NULL, fw, fl, fwt, nf);
         for (int32_t q = 0; q < L; ++q) {
             lv[q] = 0.0;
             lw[q] = 0.0;
         }
-        newton_unit(d1, d2, leaf, n, nl, scaled_l2, lv);
+        if (pairwise) pairwise_leaf_deltas(fw, fl, fwt, n_flat, leaf, d1, n, nl, a->l2_leaf_reg, lv);
+        else newton_unit(d1, d2, leaf, n, nl, scaled_l2, lv);
         for (int64_t i = 0; i < n; ++i) lw[leaf[i]] += w[i];
         if (o->raw_leaf_values) memcpy(o->raw_leaf_values + (size_t)it * L, lv, sizeof(double) * L);
         const double total = orc_sum_f64(lw, nl);
@@ -518,14 +546,15 @@ static int train_yetirank(const orc_rank_args* a, orc_rank_out* o, int32_t NB) {
         for (int32_t q = 0; q < nl; ++q) lv[q] *= lr;
         memcpy(o->leaf_values + (size_t)it * L, lv, sizeof(double) * L);
         for (int64_t i = 0; i < n; ++i) approx[i] += lv[leaf[i]];
-        /* the learning fold's own resample, Newton deltas x lr (no centring) */
-        yeti_phase_ders(a, lapprox, gw, sl, cwbuf, d1, d2, NULL);
-        newton_unit(d1, d2, leaf, n, nl, scaled_l2, lv);
+        /* the learning fold's own resample, Newton (or Cholesky) deltas x lr (no centring) */
+        yeti_phase_ders(a, lapprox, gw, sl, cwbuf, d1, d2, NULL, fw, fl, fwt, nf);
+        if (pairwise) pairwise_leaf_deltas(fw, fl, fwt, n_flat, leaf, d1, n, nl, a->l2_leaf_reg, lv);
+        else newton_unit(d1, d2, leaf, n, nl, scaled_l2, lv);
         for (int64_t i = 0; i < n; ++i) lapprox[i] += lv[leaf[i]] * lr;
         if (o->staged) memcpy(o->staged + (size_t)it * n, approx, sizeof(double) * (size_t)n);
     }
     free(w); free(gw); free(cwbuf); free(approx); free(lapprox); free(d1); free(d2); free(eff); free(tmp);
-    free(leaf); free(lv); free(lw); free(seeds);
+    free(leaf); free(lv); free(lw); free(seeds); free(fw); free(fl); free(fwt);
     return rc;
 }
 
@@ -667,8 +696,8 @@ static double pairwise_score(const double* avrg, const double* der, const double
  * calculate_pairwise_score, pairwise_scoring.rs:101-580): the bucket of a
  * row is its bin. */
 static void pairwise_feature_scores(const uint8_t* col, int64_t n, int32_t B, const int32_t* leaf_of, int32_t P,
-                                    const double* der1, const int64_t* pw, const int64_t* pl, int64_t n_pairs,
-                                    double l2, double prior, double* scores) {
+                                    const double* der1, const int64_t* pw, const int64_t* pl, const double* pwt,
+                                    int64_t n_pairs, double l2, double prior, double* scores) {
     const int32_t n2 = 2 * P;
     double* ds = (double*)calloc((size_t)P * B, sizeof(double));        /* [P][B] */
     double* sm = (double*)calloc((size_t)P * P * B, sizeof(double));    /* smaller [P][P][B] */
@@ -682,12 +711,13 @@ static void pairwise_feature_scores(const uint8_t* col, int64_t n, int32_t B, co
         const int64_t wv = pw[k], lo = pl[k];
         if (wv == lo) continue;
         const int32_t wb = col[wv], wl = leaf_of[wv], lb = col[lo], ll = leaf_of[lo];
+        const double wt = pwt ? pwt[k] : 1.0;
         if (wb > lb) {
-            sm[((size_t)ll * P + wl) * B + lb] -= 1.0;
-            gr[((size_t)ll * P + wl) * B + wb] -= 1.0;
+            sm[((size_t)ll * P + wl) * B + lb] -= wt;
+            gr[((size_t)ll * P + wl) * B + wb] -= wt;
         } else {
-            sm[((size_t)wl * P + ll) * B + wb] -= 1.0;
-            gr[((size_t)wl * P + ll) * B + lb] -= 1.0;
+            sm[((size_t)wl * P + ll) * B + wb] -= wt;
+            gr[((size_t)wl * P + ll) * B + lb] -= wt;
         }
     }
     for (int32_t q = 0; q < P; ++q) dsum[2 * q + 1] += orc_sum_f64(ds + (size_t)q * B, B);
@@ -746,10 +776,32 @@ static void pairwise_feature_scores(const uint8_t* col, int64_t n, int32_t B, co
 }
 #undef WS
 
+/* compute_pairwise_leaf_deltas (pairwise_leaves.rs:219-242): the leaf
+ * pair-weight matrix in the pairs' order, the ordered leaf der sums, the
+ * Cholesky system with the raw l2 and the 0.1 prior. */
+static void pairwise_leaf_deltas(const int64_t* pw, const int64_t* pl, const double* pwt, int64_t n_pairs,
+                                 const int32_t* leaf, const double* d1, int64_t n, int32_t nl, double l2, double* lv) {
+    double* wsum = (double*)calloc((size_t)nl * nl, sizeof(double));
+    double* dsl = (double*)calloc((size_t)nl, sizeof(double));
+    for (int64_t k = 0; k < n_pairs; ++k) {
+        const int32_t wl = leaf[pw[k]], ll = leaf[pl[k]];
+        if (wl == ll) continue;
+        const double wt = pwt ? pwt[k] : 1.0;
+        wsum[(size_t)wl * nl + ll] -= wt;
+        wsum[(size_t)ll * nl + wl] -= wt;
+        wsum[(size_t)wl * nl + wl] += wt;
+        wsum[(size_t)ll * nl + ll] += wt;
+    }
+    for (int64_t i = 0; i < n; ++i) dsl[leaf[i]] += d1[i];
+    pairwise_leaf_values(wsum, dsl, nl, l2, 0.1, lv);
+    free(wsum);
+    free(dsl);
+}
+
 /* the pairwise greedy search (tree.rs:3861-3960): per level, every feature's
  * pairwise scores, strict first-wins over (feature, border). */
 static int pairwise_search(const orc_rank_args* a, const double* der1, const int64_t* pw, const int64_t* pl,
-                           int64_t n_pairs, int32_t* feat, int32_t* sbin, int32_t* leaf_of) {
+                           const double* pwt, int64_t n_pairs, int32_t* feat, int32_t* sbin, int32_t* leaf_of) {
     const int64_t n = a->n;
     double* sc = (double*)malloc(sizeof(double) * 256);
     for (int64_t i = 0; i < n; ++i) leaf_of[i] = 0;
@@ -760,7 +812,7 @@ static int pairwise_search(const orc_rank_args* a, const double* der1, const int
         for (int32_t f = 0; f < a->n_features; ++f) {
             const int32_t nb = a->border_counts[f];
             if (nb == 0) continue;
-            pairwise_feature_scores(a->bins_fm + (size_t)f * n, n, nb + 1, leaf_of, P, der1, pw, pl, n_pairs,
+            pairwise_feature_scores(a->bins_fm + (size_t)f * n, n, nb + 1, leaf_of, P, der1, pw, pl, pwt, n_pairs,
                                     a->l2_leaf_reg, 0.1, sc);
             for (int32_t b = 0; b < nb; ++b)
                 if (sc[b] > best) {
@@ -791,7 +843,7 @@ int orc_train_ranking(const orc_rank_args* a, orc_rank_out* o) {
     int32_t NB = 1;
     for (int32_t f = 0; f < F; ++f)
         if (a->border_counts[f] + 1 > NB) NB = a->border_counts[f] + 1;
-    if (a->loss == ORC_RANK_YETIRANK) return train_yetirank(a, o, NB);
+    if (a->loss == ORC_RANK_YETIRANK || a->loss == ORC_RANK_YETIRANK_PAIRWISE) return train_yetirank(a, o, NB);
     if (a->loss == ORC_RANK_STOCHASTICRANK) return train_stochasticrank(a, o, NB);
     competitors cp = {NULL, NULL};
     const int pairlogit = a->loss == ORC_RANK_PAIRLOGIT || a->loss == ORC_RANK_PAIRLOGIT_PAIRWISE;
@@ -916,7 +968,7 @@ int orc_train_ranking(const orc_rank_args* a, orc_rank_out* o) {
         int taken;
         if (a->loss == ORC_RANK_PAIRLOGIT_PAIRWISE) {
             /* pairwise scoring over the flattened competitor pairs (tree.rs:3747-3760) */
-            taken = pairwise_search(a, d1, pairs_w, pairs_l, n_flat, tf, tb, leaf);
+            taken = pairwise_search(a, d1, pairs_w, pairs_l, NULL, n_flat, tf, tb, leaf);
             if (taken < 0) {
                 rc = -3;
                 break;
@@ -958,20 +1010,7 @@ int orc_train_ranking(const orc_rank_args* a, orc_rank_out* o) {
             /* compute_pairwise_leaf_deltas (pairwise_leaves.rs:219-242): the
              * leaf pair-weight matrix in group / winner / competitor order, the
              * ordered leaf der sums, the Cholesky system with the raw l2 */
-            double* wsum = (double*)calloc((size_t)nl * nl, sizeof(double));
-            double* dsl = (double*)calloc((size_t)nl, sizeof(double));
-            for (int64_t k = 0; k < n_flat; ++k) {
-                const int32_t wl = leaf[pairs_w[k]], ll = leaf[pairs_l[k]];
-                if (wl == ll) continue;
-                wsum[(size_t)wl * nl + ll] -= 1.0;
-                wsum[(size_t)ll * nl + wl] -= 1.0;
-                wsum[(size_t)wl * nl + wl] += 1.0;
-                wsum[(size_t)ll * nl + ll] += 1.0;
-            }
-            for (int64_t i = 0; i < n; ++i) dsl[leaf[i]] += d1[i];
-            pairwise_leaf_values(wsum, dsl, nl, a->l2_leaf_reg, 0.1, lv);
-            free(wsum);
-            free(dsl);
+            pairwise_leaf_deltas(pairs_w, pairs_l, NULL, n_flat, leaf, d1, n, nl, a->l2_leaf_reg, lv);
         }
         if (o->raw_leaf_values) memcpy(o->raw_leaf_values + (size_t)it * L, lv, sizeof(double) * L);
         /* 5. normalize_leaf_values */

@@ -93,7 +93,8 @@ class _RankOut(C.Structure):
                 ("raw_leaf_values", C.c_void_p), ("staged", C.c_void_p)]
 
 
-RANK_LOSS = {"QueryRMSE": 0, "PairLogit": 1, "PairLogitPairwise": 2, "QuerySoftMax": 3, "LambdaMart": 4, "YetiRank": 5, "StochasticRank": 6}
+RANK_LOSS = {"QueryRMSE": 0, "PairLogit": 1, "PairLogitPairwise": 2, "QuerySoftMax": 3, "LambdaMart": 4, "YetiRank": 5, "StochasticRank": 6,
+             "YetiRankPairwise": 7}
 
 
 def lib():

@@ -245,8 +245,9 @@ def ranking_fixtures(ref):
                   pairs=np.load(os.path.join(fx, "inputs/pairs.npy")).astype(np.int64))
     losses = []
     for loss in ("QueryRMSE", "PairLogit", "PairLogitPairwise", "QuerySoftMax", "LambdaMart", "YetiRank",
-                 "StochasticRank"):
-        d = {"YetiRank": "yetirank", "StochasticRank": "stochasticrank"}.get(loss, loss)
+                 "StochasticRank", "YetiRankPairwise"):
+        d = {"YetiRank": "yetirank", "StochasticRank": "stochasticrank",
+             "YetiRankPairwise": "yetirank_pairwise"}.get(loss, loss)
         cfg = json.loads(_read(os.path.join(fx, d, "config.json")))
         model = json.loads(_read(os.path.join(fx, d, "model.json")))
         mparams = model["model_info"].get("params")

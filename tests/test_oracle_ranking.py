@@ -1,5 +1,5 @@
 """Pin the oracle's grouped-loss loop (QueryRMSE, PairLogit, PairLogitPairwise, QuerySoftMax, LambdaMart, YetiRank,
-StochasticRank) to upstream.
+YetiRankPairwise, StochasticRank) to upstream.
 
 tests/golden/ranking_corpus.npz comes from the reference's frozen ranking
 corpus (crates/cb-oracle/fixtures/ranking_corpus: 12 objects in 5 contiguous
@@ -11,7 +11,8 @@ lambda ders of a stable approx-descending sort (ranking_der.rs:482-628) with
 Newton leaves; YetiRank pairs sampled per tree and phase from TFastRng64
 query seeds (crates/cb-train/src/yetirank.rs) with separate learning-fold and
 model approximants (boosting.rs:4997-5060, 7347-7420, 8070-8200, 8787-8880);
-StochasticRank's Monte-Carlo DCG ders with the same seeder's recalc bases
+YetiRankPairwise the same sampled pairs, weighted, through the pairwise
+scorer and Cholesky leaves; StochasticRank's Monte-Carlo DCG ders with the same seeder's recalc bases
 (ranking_der.rs:640-1000, boosting.rs:5065-5100).
 PairLogitPairwise scores
 splits with the pairwise statistics and a per-candidate Cholesky solve
@@ -50,7 +51,7 @@ def _fit(d, loss, borders, **kw):
         assert p["leaf_estimation_method"] == "Gradient"
         args.update(srank_metric=p["srank_metric"], srank_sigma=p["srank_sigma"], srank_mu=p["srank_mu"],
                     srank_num_estimations=p["srank_num_estimations"])
-    if loss == "YetiRank":
+    if loss in ("YetiRank", "YetiRankPairwise"):
         args.update(yeti_permutations=p["yeti_permutations"], yeti_decay=p["yeti_decay"])
     if loss == "LambdaMart":
         assert p["leaf_estimation_method"] == "Newton" and p["lambdamart_metric"] == "NDCG"
@@ -61,7 +62,7 @@ def _fit(d, loss, borders, **kw):
 
 
 @pytest.mark.parametrize("loss", ["QueryRMSE", "PairLogit", "PairLogitPairwise", "QuerySoftMax", "LambdaMart",
-                                  "YetiRank", "StochasticRank"])
+                                  "YetiRank", "StochasticRank", "YetiRankPairwise"])
 @pytest.mark.parametrize("border_set", ["full", "model"])
 def test_ranking_matches_upstream(loss, border_set):
     d = _load()
