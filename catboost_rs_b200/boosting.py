@@ -311,7 +311,8 @@ def fit_ranking(float_columns: Sequence[np.ndarray], borders: Sequence[Sequence[
                 sf[it, l], sb[it, l] = f, b
             raw[it] = tree.leaf_values
             leaf_w = np.bincount(tree.leaf_of.astype(np.int64), weights=doc_w, minlength=L)
-            lv[it] = normalize_leaf_values(p.loss in ("PairLogit", "PairLogitPairwise", "YetiRank"), lr, leaf_w,
+            lv[it] = normalize_leaf_values(p.loss in ("PairLogit", "PairLogitPairwise", "YetiRank", "YetiRankPairwise"),
+                                           lr, leaf_w,
                                            tree.leaf_values)
             if staged:
                 st[it] = rt.resident_approx()[0]

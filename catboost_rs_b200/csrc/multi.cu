@@ -505,7 +505,7 @@ __global__ void mc_apply_pending_kernel(int64_t n, int K, int L, double* __restr
 // ---- ranking mode (grouped losses, K = 1) ----------------------------------
 
 enum : int { kRankQueryRmse = 0, kRankPairLogit = 1, kRankPairLogitPairwise = 2, kRankQuerySoftMax = 3,
-             kRankLambdaMart = 4, kRankYetiRank = 5, kRankStochasticRank = 6 };
+             kRankLambdaMart = 4, kRankYetiRank = 5, kRankStochasticRank = 6, kRankYetiRankPairwise = 7 };
 
 // Per-loss parameters of rk_der_kernel.  LambdaMart's position denominators
 // log2(2 + pos) (as log(x) * log2(e), ranking_der.rs:456-467) and each group's
@@ -1035,37 +1035,74 @@ __host__ __device__ inline size_t pw_scratch_doubles(int n2) {
     return (size_t)n2 * n2 + m * m + 5 * (size_t)n2;
 }
 
-// Pair statistics of one level (compute_pair_weight_statistics,
-// pairwise_scoring.rs:163-198), buckets = bins, pair weight 1:
-//   wb > lb: smaller[ll][wl][lb] -= 1, greater[ll][wl][wb] -= 1
-//   else:    smaller[wl][ll][wb] -= 1, greater[wl][ll][lb] -= 1
-// int32 counts (exact in any order): st[f][a][c][bin][2] = (smaller, greater).
-__global__ void rk_pairstat_kernel(int64_t n_pairs, int64_t n, int P, int NB, const int64_t* __restrict__ pw,
-                                   const int64_t* __restrict__ pl, const uint8_t* __restrict__ bins_fm,
-                                   const uint16_t* __restrict__ leaf, int32_t* __restrict__ stats) {
-    const int f = blockIdx.y;
-    const uint8_t* col = bins_fm + (size_t)f * (size_t)n;
-    int32_t* st = stats + (size_t)f * P * P * NB * 2;
-    for (int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < n_pairs; k += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t w = pw[k], l = pl[k];
-        if (w == l) continue;
-        const int wb = col[w], lb = col[l], wl = leaf[w], ll = leaf[l];
-        if (wl >= P || ll >= P || wb >= NB || lb >= NB) continue;
-        if (wb > lb) {
-            atomicSub(&st[(((size_t)ll * P + wl) * NB + lb) * 2 + 0], 1);
-            atomicSub(&st[(((size_t)ll * P + wl) * NB + wb) * 2 + 1], 1);
-        } else {
-            atomicSub(&st[(((size_t)wl * P + ll) * NB + wb) * 2 + 0], 1);
-            atomicSub(&st[(((size_t)wl * P + ll) * NB + lb) * 2 + 1], 1);
-        }
+// Pair weights enter the statistics as int64 fixed point at 2^pw_shift
+// (llrint(w * 2^pw_shift)); the host bounds pw_shift so every sum stays below
+// 2^61.  Unit weights are exact, and any order gives the same sums.
+__device__ __forceinline__ void pw_add(long long* p, long long v) {
+    atomicAdd(reinterpret_cast<unsigned long long*>(p), (unsigned long long)v);
+}
+
+// One pair's statistics (compute_pair_weight_statistics,
+// pairwise_scoring.rs:163-198), buckets = bins:
+//   wb > lb: smaller[ll][wl][lb] -= w, greater[ll][wl][wb] -= w
+//   else:    smaller[wl][ll][wb] -= w, greater[wl][ll][lb] -= w
+// st[a][c][bin][2] = (smaller, greater) of one feature.
+__device__ __forceinline__ void pw_stat_pair(int wb, int lb, int wl, int ll, int P, int NB, long long q,
+                                             long long* st) {
+    if (wl >= P || ll >= P || wb >= NB || lb >= NB) return;
+    if (wb > lb) {
+        pw_add(&st[(((size_t)ll * P + wl) * NB + lb) * 2 + 0], -q);
+        pw_add(&st[(((size_t)ll * P + wl) * NB + wb) * 2 + 1], -q);
+    } else {
+        pw_add(&st[(((size_t)wl * P + ll) * NB + wb) * 2 + 0], -q);
+        pw_add(&st[(((size_t)wl * P + ll) * NB + lb) * 2 + 1], -q);
     }
 }
 
+// The statistics of one level over an explicit pair list of unit weight.
+__global__ void rk_pairstat_kernel(int64_t n_pairs, int64_t n, int P, int NB, const int64_t* __restrict__ pw,
+                                   const int64_t* __restrict__ pl, const uint8_t* __restrict__ bins_fm,
+                                   const uint16_t* __restrict__ leaf, int pw_shift, long long* __restrict__ stats) {
+    const int f = blockIdx.y;
+    const uint8_t* col = bins_fm + (size_t)f * (size_t)n;
+    long long* st = stats + (size_t)f * P * P * NB * 2;
+    const long long unit = 1ll << pw_shift;
+    for (int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < n_pairs; k += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t w = pw[k], l = pl[k];
+        if (w == l) continue;
+        pw_stat_pair(col[w], col[l], leaf[w], leaf[l], P, NB, unit, st);
+    }
+}
+
+// The statistics of one level over YetiRank's sampled pairs: a thread per
+// group walks its dense weight matrix (weight qw * cw / perms in f32).
+__global__ void rk_yeti_pairstat_kernel(int n_groups, const int64_t* __restrict__ goff,
+                                        const int64_t* __restrict__ cwoff, const float* __restrict__ cw,
+                                        const double* __restrict__ gw, int perms, int64_t n, int P, int NB,
+                                        const uint8_t* __restrict__ bins_fm, const uint16_t* __restrict__ leaf,
+                                        int pw_shift, long long* __restrict__ stats) {
+    const int gi = blockIdx.x * blockDim.x + threadIdx.x;
+    if (gi >= n_groups) return;
+    const int f = blockIdx.y;
+    const uint8_t* col = bins_fm + (size_t)f * (size_t)n;
+    long long* st = stats + (size_t)f * P * P * NB * 2;
+    const int64_t b = goff[gi], g = goff[gi + 1] - b;
+    const float* cwg = cw + cwoff[gi];
+    const float qw = __double2float_rn(gw[gi]), den = (float)perms;
+    for (int64_t wl = 0; wl < g; ++wl)
+        for (int64_t ll = 0; ll < g; ++ll) {
+            const float wf = __fdiv_rn(__fmul_rn(qw, cwg[wl * g + ll]), den);
+            if (wf == 0.0f || wl == ll) continue;
+            const long long q = llrint(ldexp((double)wf, pw_shift));
+            pw_stat_pair(col[b + wl], col[b + ll], leaf[b + wl], leaf[b + ll], P, NB, q, st);
+        }
+}
+
 // Inclusive prefix over bins of every (feature, leaf, leaf, kind) row.
-__global__ void rk_pairprefix_kernel(int64_t rows, int NB, int32_t* __restrict__ st) {
+__global__ void rk_pairprefix_kernel(int64_t rows, int NB, long long* __restrict__ st) {
     for (int64_t r = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; r < rows; r += (int64_t)gridDim.x * blockDim.x) {
-        int32_t* row = st + (size_t)(r >> 1) * NB * 2 + (r & 1);
-        int32_t run = 0;
+        long long* row = st + (size_t)(r >> 1) * NB * 2 + (r & 1);
+        long long run = 0;
         for (int b = 0; b < NB; ++b) {
             run += row[(size_t)b * 2];
             row[(size_t)b * 2] = run;
@@ -1172,18 +1209,20 @@ __device__ void pw_leaf_values_block(const double* w, const double* der, int n, 
 // One off-diagonal entry (r != c) of the pair-weight system of border b
 // (the running sums of pairwise_scoring.rs:420-540 evaluated in closed
 // form); leaf a of row r = r / 2, its side r % 2 (1: bins above b).
-__device__ __forceinline__ double pw_offdiag(int r, int c, int P, int NB, int b, const int32_t* __restrict__ st) {
+// Every off-diagonal entry is minus a pair-weight sum (<= 0), so each
+// diagonal, minus its row sum, is exact in the int64 fixed point too.
+__device__ __forceinline__ long long pw_offdiag(int r, int c, int P, int NB, int b, const long long* __restrict__ st) {
     auto S = [&](int u, int v, int bin) -> long long { return st[(((size_t)u * P + v) * NB + bin) * 2 + 0]; };
     auto G = [&](int u, int v, int bin) -> long long { return st[(((size_t)u * P + v) * NB + bin) * 2 + 1]; };
     const int a = r >> 1, sa = r & 1, d = c >> 1, sd = c & 1;
-    if (a == d) return (double)(S(a, a, b) - G(a, a, b));  // the two sides of one leaf
+    if (a == d) return S(a, a, b) - G(a, a, b);  // the two sides of one leaf
     const int y = a < d ? a : d, x = a < d ? d : a;
     const int sy = a < d ? sa : sd, sx = a < d ? sd : sa;
     if (sy == 1 && sx == 1)  // every pair between the leaves minus those at or below b
-        return (double)((S(x, y, NB - 1) + S(y, x, NB - 1)) - (S(x, y, b) + S(y, x, b)));
-    if (sy == 0 && sx == 0) return (double)(G(x, y, b) + G(y, x, b));
-    if (sx == 0) return (double)(S(x, y, b) - G(x, y, b));  // x below, y above
-    return (double)(S(y, x, b) - G(y, x, b));               // x above, y below
+        return (S(x, y, NB - 1) + S(y, x, NB - 1)) - (S(x, y, b) + S(y, x, b));
+    if (sy == 0 && sx == 0) return G(x, y, b) + G(y, x, b);
+    if (sx == 0) return S(x, y, b) - G(x, y, b);  // x below, y above
+    return S(y, x, b) - G(y, x, b);               // x above, y below
 }
 
 // Scores of every candidate (feature, border) at a level with P leaves
@@ -1193,9 +1232,9 @@ __device__ __forceinline__ double pw_offdiag(int r, int c, int P, int NB, int b,
 // Scratch: dynamic shared memory when 2P <= 64, else a global slot per block.
 __global__ void __launch_bounds__(kPwThreads)
 rk_pairscore_kernel(int P, int F, int NB, int C, const unsigned long long* __restrict__ pre,
-                    const int32_t* __restrict__ stats, const int32_t* __restrict__ border_counts,
-                    const McState* __restrict__ ms, double l2, int use_smem, double* __restrict__ gscratch,
-                    double* __restrict__ scores) {
+                    const long long* __restrict__ stats, const int32_t* __restrict__ border_counts,
+                    const McState* __restrict__ ms, double l2, int pw_shift, int use_smem,
+                    double* __restrict__ gscratch, double* __restrict__ scores) {
     extern __shared__ double pw_smem[];
     __shared__ int s_flag;
     const int n2 = 2 * P, m = n2 - 1, tid = threadIdx.x;
@@ -1207,6 +1246,7 @@ rk_pairscore_kernel(int P, int F, int NB, int C, const unsigned long long* __res
     double* x = y + n2;
     double* term = x + n2;
     const double inv = ldexp(1.0, -ms->hist_shift);
+    const double winv = ldexp(1.0, -pw_shift);
     const int64_t cand = (int64_t)F * NB;
     for (int64_t k = blockIdx.x; k < cand; k += gridDim.x) {
         const int f = (int)(k / NB), b = (int)(k - (int64_t)f * NB);
@@ -1214,22 +1254,23 @@ rk_pairscore_kernel(int P, int F, int NB, int C, const unsigned long long* __res
             if (tid == 0) scores[k] = -INFINITY;
             continue;
         }
-        const int32_t* st = stats + (size_t)f * P * P * NB * 2;
+        const long long* st = stats + (size_t)f * P * P * NB * 2;
         for (int idx = tid; idx < n2 * n2; idx += blockDim.x) {
             const int r = idx / n2, c = idx - r * n2;
-            ws[idx] = r == c ? 0.0 : pw_offdiag(r, c, P, NB, b, st);
+            if (r == c) {  // rows sum to zero: minus the exact int64 row sum
+                long long s = 0;
+                for (int cc = 0; cc < n2; ++cc)
+                    if (cc != r) s += pw_offdiag(r, cc, P, NB, b, st);
+                ws[idx] = __dmul_rn((double)(-s), winv);
+            } else {
+                ws[idx] = __dmul_rn((double)pw_offdiag(r, c, P, NB, b, st), winv);
+            }
         }
         for (int q = tid; q < P; q += blockDim.x) {
             const unsigned long long* row = pre + ((size_t)q * F + f) * NB * C;
             const long long below = (long long)row[(size_t)b * C], all = (long long)row[(size_t)(NB - 1) * C];
             dsum[2 * q] = __dmul_rn((double)below, inv);
             dsum[2 * q + 1] = __dmul_rn((double)(all - below), inv);
-        }
-        __syncthreads();
-        for (int r = tid; r < n2; r += blockDim.x) {  // rows sum to zero: exact integer diagonal
-            double s = 0.0;
-            for (int c = 0; c < n2; ++c) s = __dadd_rn(s, ws[(size_t)r * n2 + c]);
-            ws[(size_t)r * n2 + r] = -s;
         }
         __syncthreads();
         pw_leaf_values_block(ws, dsum, n2, l2, lv, A, y, x, &s_flag);
@@ -1249,18 +1290,40 @@ rk_pairscore_kernel(int P, int F, int NB, int C, const unsigned long long* __res
 }
 
 // The leaf pair-weight matrix of the grown tree (compute_pairwise_weight_sums,
-// pairwise_leaves.rs:51-91): integer counts, exact in any order.
+// pairwise_leaves.rs:51-91), int64 fixed point at 2^pw_shift: exact in any order.
+__device__ __forceinline__ void pw_leafw_pair(int wl, int ll, int L, long long q, long long* wsum) {
+    if (wl == ll || wl >= L || ll >= L) return;
+    pw_add(&wsum[(size_t)wl * L + ll], -q);
+    pw_add(&wsum[(size_t)ll * L + wl], -q);
+    pw_add(&wsum[(size_t)wl * L + wl], q);
+    pw_add(&wsum[(size_t)ll * L + ll], q);
+}
+
 __global__ void rk_pairleafw_kernel(int64_t n_pairs, int L, const int64_t* __restrict__ pw,
-                                    const int64_t* __restrict__ pl, const uint16_t* __restrict__ leaf,
-                                    int32_t* __restrict__ wsum) {
-    for (int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < n_pairs; k += (int64_t)gridDim.x * blockDim.x) {
-        const int wl = leaf[pw[k]], ll = leaf[pl[k]];
-        if (wl == ll || wl >= L || ll >= L) continue;
-        atomicSub(&wsum[(size_t)wl * L + ll], 1);
-        atomicSub(&wsum[(size_t)ll * L + wl], 1);
-        atomicAdd(&wsum[(size_t)wl * L + wl], 1);
-        atomicAdd(&wsum[(size_t)ll * L + ll], 1);
-    }
+                                    const int64_t* __restrict__ pl, const uint16_t* __restrict__ leaf, int pw_shift,
+                                    long long* __restrict__ wsum) {
+    const long long unit = 1ll << pw_shift;
+    for (int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < n_pairs; k += (int64_t)gridDim.x * blockDim.x)
+        pw_leafw_pair(leaf[pw[k]], leaf[pl[k]], L, unit, wsum);
+}
+
+// The same over YetiRank's sampled pairs (dense per-group matrices).
+__global__ void rk_yeti_pairleafw_kernel(int n_groups, const int64_t* __restrict__ goff,
+                                         const int64_t* __restrict__ cwoff, const float* __restrict__ cw,
+                                         const double* __restrict__ gw, int perms, int L,
+                                         const uint16_t* __restrict__ leaf, int pw_shift,
+                                         long long* __restrict__ wsum) {
+    const int gi = blockIdx.x * blockDim.x + threadIdx.x;
+    if (gi >= n_groups) return;
+    const int64_t b = goff[gi], g = goff[gi + 1] - b;
+    const float* cwg = cw + cwoff[gi];
+    const float qw = __double2float_rn(gw[gi]), den = (float)perms;
+    for (int64_t wl = 0; wl < g; ++wl)
+        for (int64_t ll = 0; ll < g; ++ll) {
+            const float wf = __fdiv_rn(__fmul_rn(qw, cwg[wl * g + ll]), den);
+            if (wf == 0.0f) continue;
+            pw_leafw_pair(leaf[b + wl], leaf[b + ll], L, llrint(ldexp((double)wf, pw_shift)), wsum);
+        }
 }
 
 // Cholesky pairwise leaves (compute_pairwise_leaf_deltas, pairwise_leaves.rs:
@@ -1269,18 +1332,19 @@ __global__ void rk_pairleafw_kernel(int64_t n_pairs, int L, const int64_t* __res
 // normalize_leaf_values' document-weighted centring x lr (boosting.rs:
 // 2844-2880).  scratch: pw_scratch_doubles(L).
 __global__ void __launch_bounds__(kPwThreads)
-rk_pairleaf_kernel(int L, const int32_t* __restrict__ wsum, const unsigned long long* __restrict__ sums,
-                   const McState* __restrict__ ms, double l2, double lr, double* __restrict__ scratch,
-                   double* __restrict__ leaf_raw, double* __restrict__ leaf_lrv) {
+rk_pairleaf_kernel(int L, const long long* __restrict__ wsum, const unsigned long long* __restrict__ sums,
+                   const McState* __restrict__ ms, double l2, double lr, int pw_shift, int centre_on,
+                   double* __restrict__ scratch, double* __restrict__ leaf_raw, double* __restrict__ leaf_lrv) {
     __shared__ int s_flag;
     const int m = L - 1, tid = threadIdx.x;
     const double inv = ldexp(1.0, -ms->leaf_shift);
+    const double winv = ldexp(1.0, -pw_shift);
     double* w = scratch;
     double* A = w + (size_t)L * L;
     double* der = A + (size_t)(m > 0 ? m : 1) * (m > 0 ? m : 1);
     double* y = der + L;
     double* x = y + L;
-    for (int k = tid; k < L * L; k += blockDim.x) w[k] = (double)wsum[k];
+    for (int k = tid; k < L * L; k += blockDim.x) w[k] = __dmul_rn((double)wsum[k], winv);
     for (int q = tid; q < L; q += blockDim.x) der[q] = __dmul_rn((double)(long long)sums[3 * q], inv);
     __syncthreads();
     pw_leaf_values_block(w, der, L, l2, leaf_raw, A, y, x, &s_flag);
@@ -1288,7 +1352,7 @@ rk_pairleaf_kernel(int L, const int32_t* __restrict__ wsum, const unsigned long 
     double total = 0.0;
     for (int q = 0; q < L; ++q) total = __dadd_rn(total, __dmul_rn((double)(long long)sums[3 * q + 2], inv));
     double avg = 0.0;
-    const bool centre = fabs(total) > 1e-9;
+    const bool centre = centre_on && fabs(total) > 1e-9;
     if (centre) {
         double acc = 0.0;
         for (int q = 0; q < L; ++q)
@@ -1348,7 +1412,8 @@ struct cbgpu_multi_session {
     // the level's pair statistics, the leaf pair-weight matrix, scratch
     int64_t n_pairs = 0;
     int64_t* d_pwin = nullptr;
-    int32_t *d_pstat = nullptr, *d_pwsum = nullptr;
+    long long *d_pstat = nullptr, *d_pwsum = nullptr;
+    int pw_shift = 0;  // pair weights in the statistics: llrint(w * 2^pw_shift)
     double* d_pwscratch = nullptr;
     double raw_l2 = 0.0;
     double sm_lambda = 0.01, sm_beta = 1.0;
@@ -1656,6 +1721,7 @@ int cbgpu_rank_begin_raw(const cbgpu_begin_args* a, const int64_t* group_offsets
     else if (a->loss == CBGPU_LOSS_LAMBDAMART) mode = kRankLambdaMart;
     else if (a->loss == CBGPU_LOSS_YETIRANK) mode = kRankYetiRank;
     else if (a->loss == CBGPU_LOSS_STOCHASTICRANK) mode = kRankStochasticRank;
+    else if (a->loss == CBGPU_LOSS_YETIRANK_PAIRWISE) mode = kRankYetiRankPairwise;
     else return mfail(CBGPU_DECLINED, "rank_begin: loss %d is not a covered grouped loss", a->loss);
     const double l2_leaf_reg = params && params->l2_leaf_reg >= 0.0 ? params->l2_leaf_reg : a->scaled_l2;
     const double sm_lambda = params ? params->softmax_lambda : 0.01;
@@ -1667,7 +1733,7 @@ int cbgpu_rank_begin_raw(const cbgpu_begin_args* a, const int64_t* group_offsets
     const int64_t lm_top = params ? params->lambdamart_top : -1;
     const int yeti_perms = params ? params->yeti_permutations : 10;
     const double yeti_decay = params ? params->yeti_decay : 0.85;
-    if (mode == kRankYetiRank) {
+    if (mode == kRankYetiRank || mode == kRankYetiRankPairwise) {
         if (yeti_perms < 1 || !std::isfinite(yeti_decay))
             return mfail(CBGPU_ERR_INVALID, "rank_begin: YetiRank needs permutations >= 1 and a finite decay");
         int64_t cells = 0;
@@ -1702,7 +1768,7 @@ int cbgpu_rank_begin_raw(const cbgpu_begin_args* a, const int64_t* group_offsets
     if (a->world_size != 1) return mfail(CBGPU_DECLINED, "rank_begin: one GPU per ranking session");
     if (a->depth < 1 || a->depth > kMcMaxDepth)
         return mfail(CBGPU_DECLINED, "rank_begin: depth %d outside 1..%d", a->depth, kMcMaxDepth);
-    if (mode == kRankPairLogitPairwise) {
+    if (mode == kRankPairLogitPairwise || mode == kRankYetiRankPairwise) {
         if (a->depth > kPwMaxDepth)
             return mfail(CBGPU_DECLINED, "rank_begin: pairwise scoring covers depth 1..%d, got %d", kPwMaxDepth,
                          a->depth);
@@ -1714,7 +1780,7 @@ int cbgpu_rank_begin_raw(const cbgpu_begin_args* a, const int64_t* group_offsets
         int maxb = 0;
         for (int f = 0; f < a->n_features; ++f) maxb = std::max(maxb, (int)border_counts[f]);
         const size_t P = (size_t)1 << (a->depth - 1);
-        const size_t bytes = (size_t)a->n_features * P * P * (size_t)(maxb + 1) * 2 * sizeof(int32_t);
+        const size_t bytes = (size_t)a->n_features * P * P * (size_t)(maxb + 1) * 2 * sizeof(long long);
         if (bytes > kPwMaxStatBytes)
             return mfail(CBGPU_DECLINED, "rank_begin: pair statistics need %zu bytes (> %zu)", bytes,
                          kPwMaxStatBytes);
@@ -1801,7 +1867,7 @@ int cbgpu_rank_begin_raw(const cbgpu_begin_args* a, const int64_t* group_offsets
         if (!rc) rc = mdalloc(&s->d_eff, (size_t)n);
         if (!rc) rc = mdalloc(&s->d_der2, (size_t)n);
         if (!rc) rc = mdalloc(&s->d_tgt, (size_t)n);
-        if (!rc && mode == kRankYetiRank) {
+        if (!rc && (mode == kRankYetiRank || mode == kRankYetiRankPairwise)) {
             // group weight: the mean member weight (query_info.rs:180-187)
             std::vector<double> gw((size_t)n_groups);
             std::vector<int64_t> cwoff((size_t)n_groups);
@@ -1846,13 +1912,19 @@ int cbgpu_rank_begin_raw(const cbgpu_begin_args* a, const int64_t* group_offsets
                            cudaSuccess)
                 rc = mfail(CBGPU_ERR_CUDA, "rank_begin: upload failed");
         }
-        if (!rc && mode == kRankPairLogitPairwise) {
+        if (!rc && (mode == kRankPairLogitPairwise || mode == kRankYetiRankPairwise)) {
             const int L = 1 << a->depth, P = L / 2;
-            s->n_pairs = n_pairs;
             s->raw_l2 = l2_leaf_reg;
             const size_t leaf_scratch = pw_scratch_doubles(L);
             const size_t score_scratch = L > kPwSmemMaxN2 ? (size_t)kPwGlobalBlocks * pw_scratch_doubles(L) : 0;
-            rc = mdalloc(&s->d_pwin, win.size());
+            if (mode == kRankPairLogitPairwise) {
+                // unit weights: sums of at most n_pairs units stay below 2^60
+                s->n_pairs = n_pairs;
+                int t = 0;
+                while (t < 62 && ((int64_t)1 << t) < n_pairs + 1) ++t;
+                s->pw_shift = 59 - t;
+                rc = mdalloc(&s->d_pwin, win.size());
+            }
             if (!rc) rc = mdalloc(&s->d_pstat, (size_t)a->n_features * P * P * s->NB * 2);
             if (!rc) rc = mdalloc(&s->d_pwsum, (size_t)L * L);
             if (!rc) rc = mdalloc(&s->d_pwscratch, std::max(leaf_scratch, score_scratch));
@@ -1926,6 +1998,34 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
             MCU(cudaMemcpyAsync(s->d_lmideal, ideal.data(), sizeof(double) * (size_t)G, cudaMemcpyHostToDevice, st));
             MCU(cudaStreamSynchronize(st));
         }
+        if (s->rank_mode == kRankYetiRankPairwise) {
+            // a bound on any sampled pair weight: qw * 0.15 * |rel_a - rel_b| *
+            // decay^k per permutation, averaged over the permutations
+            // (yetirank.rs:450-514), and on the pair count: the cells of the
+            // groups' dense matrices; their product stays below 2^60
+            double tmin = INFINITY, tmax = -INFINITY, gwmax = 0.0, cells = 0.0;
+            int64_t maxg = 1;
+            for (int64_t i = 0; i < n; ++i) {
+                tmin = std::min(tmin, (double)(float)target[i]);
+                tmax = std::max(tmax, (double)(float)target[i]);
+            }
+            std::vector<double> gw((size_t)s->n_groups);
+            MCU(cudaMemcpy(gw.data(), s->d_gw, sizeof(double) * gw.size(), cudaMemcpyDeviceToHost));
+            for (int g = 0; g < s->n_groups; ++g) {
+                const int64_t sz = s->h_goff[(size_t)g + 1] - s->h_goff[(size_t)g];
+                gwmax = std::max(gwmax, std::fabs(gw[(size_t)g]));
+                maxg = std::max(maxg, sz);
+                cells += (double)sz * (double)sz;
+            }
+            const double decay_max = s->yeti_decay > 1.0 ? std::pow(s->yeti_decay, (double)std::max<int64_t>(maxg - 2, 0))
+                                                         : 1.0;
+            const double bound = std::max(1e-300, 1.01 * gwmax * 0.15 * (tmax - tmin) * decay_max);
+            int e = 0, t = 0;
+            std::frexp(bound, &e);
+            while (t < 62 && std::ldexp(1.0, t) < cells + 1.0) ++t;
+            s->pw_shift = std::min(60 - e - t, 1000);
+            if (s->pw_shift < 0) return mfail(CBGPU_DECLINED, "YetiRankPairwise: pair weights too large (%g)", bound);
+        }
         MCU(cudaMemcpyAsync(s->d_tgt, target, sizeof(double) * n, cudaMemcpyHostToDevice, st));
         MCU(cudaStreamSynchronize(st));
         s->target_ready = true;
@@ -1972,7 +2072,7 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
     MCU(cudaMemcpyAsync(s->d_tp, s->h_tp, sizeof(TreeParams), cudaMemcpyHostToDevice, st));
     MCU(cudaMemsetAsync(s->d_ms, 0, sizeof(McState), st));
     const unsigned g = grid_for(n);
-    const bool yeti = s->rank_mode == kRankYetiRank;
+    const bool yeti = s->rank_mode == kRankYetiRank || s->rank_mode == kRankYetiRankPairwise;
     const bool srank = s->rank_mode == kRankStochasticRank;
     const unsigned yg = (unsigned)((s->n_groups + 127) / 128);
     uint64_t srank_base[2] = {0, 0};
@@ -2043,7 +2143,7 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
     mc_pack_kernel<<<g, kMcThreads, 0, st>>>(n, K, s->wd1, hw, s_mode, s->sw32, s->sw64, s->d_ms, s->q);
     MCU(cudaGetLastError());
     const unsigned chunks = (unsigned)((n + kMcChunk - 1) / kMcChunk);
-    const bool pairwise = s->rank_mode == kRankPairLogitPairwise;
+    const bool pairwise = s->rank_mode == kRankPairLogitPairwise || s->rank_mode == kRankYetiRankPairwise;
     for (int l = 0; l < D; ++l) {
         const int leaves = 1 << l;
         const size_t cells = (size_t)leaves * F * NB * C;
@@ -2059,17 +2159,22 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
         mc_prefix_kernel<<<grid_for((int64_t)leaves * F * C), kMcThreads, 0, st>>>(leaves, F, NB, C, s->hist);
         if (pairwise) {
             const int64_t rows = (int64_t)F * leaves * leaves * 2;
-            MCU(cudaMemsetAsync(s->d_pstat, 0, sizeof(int32_t) * (size_t)rows * NB, st));
-            rk_pairstat_kernel<<<dim3(grid_for(s->n_pairs), (unsigned)F), kMcThreads, 0, st>>>(
-                s->n_pairs, n, leaves, NB, s->d_pwin, s->d_closer, s->bins_fm, s->leaf, s->d_pstat);
+            MCU(cudaMemsetAsync(s->d_pstat, 0, sizeof(long long) * (size_t)rows * NB, st));
+            if (yeti)
+                rk_yeti_pairstat_kernel<<<dim3(yg, (unsigned)F), 128, 0, st>>>(
+                    s->n_groups, s->d_goff, s->d_cwoff, s->d_cw, s->d_gw, s->yeti_perms, n, leaves, NB, s->bins_fm,
+                    s->leaf, s->pw_shift, s->d_pstat);
+            else
+                rk_pairstat_kernel<<<dim3(grid_for(s->n_pairs), (unsigned)F), kMcThreads, 0, st>>>(
+                    s->n_pairs, n, leaves, NB, s->d_pwin, s->d_closer, s->bins_fm, s->leaf, s->pw_shift, s->d_pstat);
             rk_pairprefix_kernel<<<grid_for(rows), kMcThreads, 0, st>>>(rows, NB, s->d_pstat);
             const int n2 = 2 * leaves;
             const int pw_smem = n2 <= kPwSmemMaxN2 ? 1 : 0;
             const int64_t cand = (int64_t)F * NB;
             const int64_t blocks = std::min<int64_t>(cand, pw_smem ? (int64_t)148 * 8 : (int64_t)kPwGlobalBlocks);
             rk_pairscore_kernel<<<(unsigned)blocks, kPwThreads, pw_smem ? pw_scratch_doubles(n2) * sizeof(double) : 0,
-                                  st>>>(leaves, F, NB, C, s->hist, s->d_pstat, s->d_bc, s->d_ms, s->raw_l2, pw_smem,
-                                        s->d_pwscratch, s->scores);
+                                  st>>>(leaves, F, NB, C, s->hist, s->d_pstat, s->d_bc, s->d_ms, s->raw_l2,
+                                        s->pw_shift, pw_smem, s->d_pwscratch, s->scores);
         } else {
             mc_score_kernel<<<grid_for((int64_t)F * NB), kMcThreads, 0, st>>>(leaves, F, NB, K, s->hist, s->d_bc,
                                                                               s->d_ms, s->l2, s->score_fn, s->F0,
@@ -2080,10 +2185,8 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
         MCU(cudaGetLastError());
     }
     if (s->rank_mode >= 0) {
-        // Newton leaves over the grouped ders, then normalize_leaf_values
-        rk_leafmax_kernel<<<g, kMcThreads, 0, st>>>(n, s->wd1, s->d_der2, s->weight, s->d_ms);
-        rk_leafshift_kernel<<<1, 1, 0, st>>>(n, s->d_ms);
-        MCU(cudaMemsetAsync(s->sums, 0, sizeof(unsigned long long) * 3 * (size_t)L, st));
+        // Newton leaves over the grouped ders, then normalize_leaf_values; the
+        // leaf-value recomputes come first so the leaf fixed point sees their ders
         if (yeti) {  // the stored leaves come from pairs sampled off the model approximant
             rk_yeti_sample_kernel<<<yg, 128, 0, st>>>(s->n_groups, s->d_goff, s->approx, s->d_tgt, s->yeti_perms,
                                                      s->yeti_decay, s->d_yseeds + 2 * (size_t)s->n_groups, s->d_cwoff,
@@ -2097,14 +2200,21 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
                                                s->d_lmden, s->d_lmideal, s->d_srank_ws, s->d_lmorder, s->wd1,
                                                s->d_der2, s->d_ms);
         const int gradient = (s->rank_mode == kRankQuerySoftMax || srank) ? 1 : 0;
+        rk_leafmax_kernel<<<g, kMcThreads, 0, st>>>(n, s->wd1, s->d_der2, s->weight, s->d_ms);
+        rk_leafshift_kernel<<<1, 1, 0, st>>>(n, s->d_ms);
+        MCU(cudaMemsetAsync(s->sums, 0, sizeof(unsigned long long) * 3 * (size_t)L, st));
         rk_leafsum_kernel<<<g, kMcThreads, 0, st>>>(n, L, s->wd1, s->d_der2, s->weight, s->leaf, gradient, s->sums,
                                                     s->d_ms);
         if (pairwise) {
-            MCU(cudaMemsetAsync(s->d_pwsum, 0, sizeof(int32_t) * (size_t)L * L, st));
-            rk_pairleafw_kernel<<<grid_for(s->n_pairs), kMcThreads, 0, st>>>(s->n_pairs, L, s->d_pwin, s->d_closer,
-                                                                            s->leaf, s->d_pwsum);
+            MCU(cudaMemsetAsync(s->d_pwsum, 0, sizeof(long long) * (size_t)L * L, st));
+            if (yeti)
+                rk_yeti_pairleafw_kernel<<<yg, 128, 0, st>>>(s->n_groups, s->d_goff, s->d_cwoff, s->d_cw, s->d_gw,
+                                                            s->yeti_perms, L, s->leaf, s->pw_shift, s->d_pwsum);
+            else
+                rk_pairleafw_kernel<<<grid_for(s->n_pairs), kMcThreads, 0, st>>>(
+                    s->n_pairs, L, s->d_pwin, s->d_closer, s->leaf, s->pw_shift, s->d_pwsum);
             rk_pairleaf_kernel<<<1, kPwThreads, 0, st>>>(L, s->d_pwsum, s->sums, s->d_ms, s->raw_l2, s->lr,
-                                                         s->d_pwscratch, s->leaf_raw, s->leaf_lrv);
+                                                         s->pw_shift, 1, s->d_pwscratch, s->leaf_raw, s->leaf_lrv);
         } else {
             rk_newton_kernel<<<1, 1, 0, st>>>(L, (s->rank_mode == kRankPairLogit || yeti) ? 1 : 0, gradient, s->sums,
                                               s->d_ms, s->l2, s->lr, s->leaf_raw, s->leaf_lrv);
@@ -2121,7 +2231,17 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
             MCU(cudaMemsetAsync(s->sums, 0, sizeof(unsigned long long) * 3 * (size_t)L, st));
             rk_leafsum_kernel<<<g, kMcThreads, 0, st>>>(n, L, s->wd1, s->d_der2, s->weight, s->leaf, 0, s->sums,
                                                         s->d_ms);
-            rk_newton_kernel<<<1, 1, 0, st>>>(L, 0, 0, s->sums, s->d_ms, s->l2, s->lr, s->d_ylf_raw, s->d_ylf_lrv);
+            if (pairwise) {  // YetiRankPairwise: Cholesky deltas for the learning fold too
+                MCU(cudaMemsetAsync(s->d_pwsum, 0, sizeof(long long) * (size_t)L * L, st));
+                rk_yeti_pairleafw_kernel<<<yg, 128, 0, st>>>(s->n_groups, s->d_goff, s->d_cwoff, s->d_cw, s->d_gw,
+                                                            s->yeti_perms, L, s->leaf, s->pw_shift, s->d_pwsum);
+                rk_pairleaf_kernel<<<1, kPwThreads, 0, st>>>(L, s->d_pwsum, s->sums, s->d_ms, s->raw_l2, s->lr,
+                                                             s->pw_shift, 0, s->d_pwscratch, s->d_ylf_raw,
+                                                             s->d_ylf_lrv);
+            } else {
+                rk_newton_kernel<<<1, 1, 0, st>>>(L, 0, 0, s->sums, s->d_ms, s->l2, s->lr, s->d_ylf_raw,
+                                                  s->d_ylf_lrv);
+            }
             mc_apply_pending_kernel<<<g, kMcThreads, 0, st>>>(n, 1, L, s->d_lapprox, s->leaf, s->d_ylf_lrv);
         }
         MCU(cudaGetLastError());

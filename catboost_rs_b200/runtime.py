@@ -20,7 +20,7 @@ from . import _lib
 
 LOSS = {"RMSE": 0, "Rmse": 0, "Logloss": 1, "CrossEntropy": 2, "MultiClass": 3, "QueryRMSE": 4, "PairLogit": 5,
         "PairLogitPairwise": 6, "QuerySoftMax": 7,
-        "LambdaMart": 8, "YetiRank": 9, "StochasticRank": 10}
+        "LambdaMart": 8, "YetiRank": 9, "StochasticRank": 10, "YetiRankPairwise": 11}
 LAMBDAMART_METRIC = {"NDCG": 0, "DCG": 1, "MRR": 2, "ERR": 3, "MAP": 4}
 SCORE = {"Cosine": 0, "L2": 1, "SolarL2": 2, "NewtonL2": 3, "NewtonCosine": 4, "LOOL2": 5, "SatL2": 6}
 BOOT = {"No": 0, "Bayesian": 1, "Bernoulli": 2, "MVS": 3, "Mvs": 3, "Poisson": 4}

@@ -52,7 +52,7 @@ typedef enum {
     CBGPU_LOSS_RMSE = 0, CBGPU_LOSS_LOGLOSS = 1, CBGPU_LOSS_CROSSENTROPY = 2, CBGPU_LOSS_MULTICLASS = 3,
     CBGPU_LOSS_QUERYRMSE = 4, CBGPU_LOSS_PAIRLOGIT = 5, CBGPU_LOSS_PAIRLOGIT_PAIRWISE = 6,
     CBGPU_LOSS_QUERYSOFTMAX = 7, CBGPU_LOSS_LAMBDAMART = 8, CBGPU_LOSS_YETIRANK = 9,
-    CBGPU_LOSS_STOCHASTICRANK = 10
+    CBGPU_LOSS_STOCHASTICRANK = 10, CBGPU_LOSS_YETIRANK_PAIRWISE = 11
 } cbgpu_loss;
 
 /* EScoreFunction (runtime.rs:834-864); Cosine is the default. */
@@ -326,6 +326,8 @@ typedef struct {
  * query seeds of YetiRankTreeSeeder (crates/cb-train/src/yetirank.rs), keeps
  * the learning-fold approximant beside the model's, and takes Newton leaves
  * (boosting.rs:7347-7420, 8070-8200, 8787-8880); explicit pairs are not used.
+ * YetiRankPairwise takes the same resamples through the pairwise scorer and
+ * Cholesky pairwise leaves, for the stored leaves and the learning fold.
  * StochasticRank draws each group's Monte-Carlo noise on the device from the
  * same seeder's recalc bases (boosting.rs:5065-5100) and takes Gradient
  * leaves.

@@ -1,5 +1,5 @@
-"""The grouped-loss (QueryRMSE, QuerySoftMax, LambdaMart, YetiRank, StochasticRank, PairLogit, PairLogitPairwise)
-device mode against upstream and the oracle.
+"""The grouped-loss (QueryRMSE, QuerySoftMax, LambdaMart, YetiRank, YetiRankPairwise, StochasticRank, PairLogit,
+PairLogitPairwise) device mode against upstream and the oracle.
 
 The device mode (csrc/multi.cu, cbgpu_rank_begin_raw) reproduces cb-train's
 grouped CPU branch: grouped ders (crates/cb-compute/src/ranking_der.rs),
@@ -35,7 +35,7 @@ def cb():
 
 
 @pytest.mark.parametrize("loss", ["QueryRMSE", "PairLogit", "PairLogitPairwise", "QuerySoftMax", "LambdaMart",
-                                  "YetiRank", "StochasticRank"])
+                                  "YetiRank", "StochasticRank", "YetiRankPairwise"])
 def test_ranking_fixture(cb, loss):
     z = np.load(GOLDEN)
     p = json.loads(str(z[f"{loss}__params"]))
@@ -156,6 +156,31 @@ def test_yetirank_matches_oracle(cb, perms, decay, weighted):
     o = oracle.train_ranking(bins, [len(b) for b in borders], y, offsets, loss="YetiRank", depth=5, iterations=4,
                              learning_rate=0.3, l2_leaf_reg=1.0, random_seed=11, weights=w,
                              yeti_permutations=perms, yeti_decay=decay)
+    np.testing.assert_array_equal(m.split_feature, o.split_feature)
+    np.testing.assert_array_equal(m.split_bin, o.split_bin)
+    assert np.max(np.abs(m.raw_leaf_values - o.raw_leaf_values)) <= TOL
+    assert np.max(np.abs(m.leaf_values - o.leaf_values)) <= TOL
+    assert np.max(np.abs(m.staged - o.staged)) <= TOL
+
+
+@pytest.mark.parametrize("depth,weighted", [(4, False), (6, True)])
+def test_yetirank_pairwise_matches_oracle(cb, depth, weighted):
+    # YetiRank's device resamples through the pairwise scorer with weighted
+    # int64 pair statistics and Cholesky leaves (stored and learning fold)
+    X, y, offsets, pairs = _ranking_data(50, 6, 61 + depth)
+    n, F = X.shape
+    w = None
+    if weighted:
+        gw = np.random.RandomState(8).choice([0.5, 1.0, 2.0], size=offsets.size - 1)
+        w = np.repeat(gw, np.diff(offsets))
+    borders = [oracle.select_borders(X[:, f], 24) for f in range(F)]
+    fp = cb.FitParams(loss="YetiRankPairwise", depth=depth, iterations=3, learning_rate=0.3, l2_leaf_reg=1.0,
+                      random_seed=5, boost_from_average=False, yeti_permutations=4)
+    m = cb.fit_ranking([X[:, f].copy() for f in range(F)], borders, y, offsets, fp, weights=w, staged=True)
+    bins = oracle.quantize(X.T.copy(), borders)
+    o = oracle.train_ranking(bins, [len(b) for b in borders], y, offsets, loss="YetiRankPairwise", depth=depth,
+                             iterations=3, learning_rate=0.3, l2_leaf_reg=1.0, random_seed=5, weights=w,
+                             yeti_permutations=4)
     np.testing.assert_array_equal(m.split_feature, o.split_feature)
     np.testing.assert_array_equal(m.split_bin, o.split_bin)
     assert np.max(np.abs(m.raw_leaf_values - o.raw_leaf_values)) <= TOL
