@@ -81,6 +81,28 @@ struct Rng64 {
     }
 };
 
+// The per-leaf terms of the SolarL2 / LOOL2 / SatL2 split scores
+// (crates/cb-compute/src/score.rs:266-330, after score_calcers.cuh), over a
+// leaf's weighted der sum and weight; score = the sum of the terms, no l2.
+// score_fn: 2 = SolarL2, 5 = LOOL2, 6 = SatL2.
+__device__ __forceinline__ double gpu_score_term(int score_fn, double sum, double weight) {
+    const double nss = __dmul_rn(-sum, sum);
+    if (score_fn == 2)
+        return weight > 1e-20
+                   ? __ddiv_rn(__dmul_rn(nss, __dadd_rn(1.0, __dmul_rn(2.0, log(__dadd_rn(weight, 1.0))))), weight)
+                   : 0.0;
+    double adjust;
+    if (score_fn == 5) {
+        adjust = weight > 1.0 ? __ddiv_rn(weight, __dsub_rn(weight, 1.0)) : 0.0;
+        adjust = __dmul_rn(adjust, adjust);
+    } else {
+        adjust = weight > 2.0 ? __ddiv_rn(__dmul_rn(weight, __dsub_rn(weight, 2.0)),
+                                          __dadd_rn(__dsub_rn(__dmul_rn(weight, weight), __dmul_rn(3.0, weight)), 1.0))
+                              : 0.0;
+    }
+    return weight > 0.0 ? __ddiv_rn(__dmul_rn(adjust, nss), weight) : 0.0;
+}
+
 // (GenRand() >> 11) * (1 / (2^53 - 1)) (rng.rs:256-259).
 __device__ __forceinline__ double real1(Rng64& r) {
     return __dmul_rn((double)(r.gen() >> 11), 1.0 / 9007199254740991.0);

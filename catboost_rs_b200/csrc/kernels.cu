@@ -1087,9 +1087,13 @@ __global__ void __launch_bounds__(kScoreWarps * 32) score_kernel(int level, int3
                     }
                     const double swd = __dmul_rn((double)pg, ig);
                     const double sw = __dmul_rn((double)ph, ih);
-                    const double avg = sw > 0.0 ? __ddiv_rn(swd, __dadd_rn(sw, l2)) : 0.0;
-                    s_num[cc][lane] = __dmul_rn(avg, swd);
-                    s_den[cc][lane] = __dmul_rn(__dmul_rn(avg, avg), sw);
+                    if (score_fn <= 1) {  // Cosine / L2
+                        const double avg = sw > 0.0 ? __ddiv_rn(swd, __dadd_rn(sw, l2)) : 0.0;
+                        s_num[cc][lane] = __dmul_rn(avg, swd);
+                        s_den[cc][lane] = __dmul_rn(__dmul_rn(avg, avg), sw);
+                    } else {  // SolarL2 / LOOL2 / SatL2: the sum of per-leaf terms
+                        s_num[cc][lane] = gpu_score_term(score_fn, swd, sw);
+                    }
                 }
             }
             __syncthreads();

@@ -308,15 +308,19 @@ __global__ void mc_score_kernel(int parents, int F, int NB, int K, const unsigne
                             w = __dmul_rn((double)(side ? wt - wp : wp), inv);
                             s = __dmul_rn((double)(side ? st - sp : sp), inv);
                         }
+                        if (score_fn > 1) {  // SolarL2 / LOOL2 / SatL2: per-leaf terms, no l2
+                            num = __dadd_rn(num, gpu_score_term(score_fn, s, w));
+                            continue;
+                        }
                         const double avg = mc_avg(s, w, l2);
                         if (pass == 0) num = __dadd_rn(num, __dmul_rn(avg, s));
                         else den = __dadd_rn(den, __dmul_rn(__dmul_rn(avg, avg), w));
                     }
                 }
             }
-            if (score_fn == CBGPU_SCORE_L2) break;
+            if (score_fn != CBGPU_SCORE_COSINE) break;
         }
-        scores[k] = score_fn == CBGPU_SCORE_L2 ? num : __ddiv_rn(num, sqrt(den));
+        scores[k] = score_fn != CBGPU_SCORE_COSINE ? num : __ddiv_rn(num, sqrt(den));
     }
 }
 
@@ -1664,7 +1668,9 @@ int cbgpu_multi_begin_cat_raw(const cbgpu_begin_args* a, int32_t approx_dim, con
     if (a->loss != CBGPU_LOSS_MULTICLASS) return mfail(CBGPU_DECLINED, "multi_begin: loss is not MultiClass");
     if (a->grow_policy != CBGPU_GROW_SYMMETRIC || !a->boosting_type_is_plain || a->fold_count != 1)
         return mfail(CBGPU_DECLINED, "multi_begin: only Plain SymmetricTree with one fold");
-    if (a->score_function != CBGPU_SCORE_COSINE && a->score_function != CBGPU_SCORE_L2)
+    if (a->score_function != CBGPU_SCORE_COSINE && a->score_function != CBGPU_SCORE_L2 &&
+        a->score_function != CBGPU_SCORE_SOLAR_L2 && a->score_function != CBGPU_SCORE_LOO_L2 &&
+        a->score_function != CBGPU_SCORE_SAT_L2)
         return mfail(CBGPU_DECLINED, "multi_begin: score function not covered");
     if (a->random_strength != 0.0) return mfail(CBGPU_DECLINED, "multi_begin: random_strength != 0");
     if (a->bootstrap_type == CBGPU_BOOT_MVS || a->bootstrap_type == CBGPU_BOOT_POISSON)
@@ -1761,7 +1767,9 @@ int cbgpu_rank_begin_raw(const cbgpu_begin_args* a, const int64_t* group_offsets
     }
     if (a->grow_policy != CBGPU_GROW_SYMMETRIC || !a->boosting_type_is_plain || a->fold_count != 1)
         return mfail(CBGPU_DECLINED, "rank_begin: only Plain SymmetricTree with one fold");
-    if (a->score_function != CBGPU_SCORE_COSINE && a->score_function != CBGPU_SCORE_L2)
+    if (a->score_function != CBGPU_SCORE_COSINE && a->score_function != CBGPU_SCORE_L2 &&
+        a->score_function != CBGPU_SCORE_SOLAR_L2 && a->score_function != CBGPU_SCORE_LOO_L2 &&
+        a->score_function != CBGPU_SCORE_SAT_L2)
         return mfail(CBGPU_DECLINED, "rank_begin: score function not covered");
     if (a->random_strength != 0.0 || a->bootstrap_type != CBGPU_BOOT_NO || a->sample_from_host)
         return mfail(CBGPU_DECLINED, "rank_begin: bootstrap / random_strength not covered on this arm");

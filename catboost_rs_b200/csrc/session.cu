@@ -228,7 +228,9 @@ int check_args(const cbgpu_begin_args* a) {
     if (!a->boosting_type_is_plain) return fail(CBGPU_DECLINED, "Ordered boosting is not covered");
     if (a->fold_count != 1) return fail(CBGPU_DECLINED, "fold_count %d != 1", a->fold_count);
     if (a->loss < 0 || a->loss > 2) return fail(CBGPU_DECLINED, "loss %d not covered", a->loss);
-    if (a->score_function != CBGPU_SCORE_COSINE && a->score_function != CBGPU_SCORE_L2)
+    if (a->score_function != CBGPU_SCORE_COSINE && a->score_function != CBGPU_SCORE_L2 &&
+        a->score_function != CBGPU_SCORE_SOLAR_L2 && a->score_function != CBGPU_SCORE_LOO_L2 &&
+        a->score_function != CBGPU_SCORE_SAT_L2)
         return fail(CBGPU_DECLINED, "score function %d not covered", a->score_function);
     if (a->depth < 1 || a->depth > 16) return fail(CBGPU_DECLINED, "depth %d outside 1..16", a->depth);
     if (a->n_bins < 2 || a->n_bins > 256)

@@ -402,10 +402,28 @@ static inline double calc_average(double sum_delta, double count, double l2) {
     return count > 0.0 ? sum_delta / (count + l2) : 0.0;
 }
 
+double orc_score_term(int32_t score_fn, double sum, double weight) {
+    if (score_fn == ORC_SCORE_SOLAR_L2)
+        return weight > 1e-20 ? (-sum * sum) * (1.0 + 2.0 * log(weight + 1.0)) / weight : 0.0;
+    double adjust;
+    if (score_fn == ORC_SCORE_LOO_L2) {
+        adjust = weight > 1.0 ? weight / (weight - 1.0) : 0.0;
+        adjust *= adjust;
+    } else {
+        adjust = weight > 2.0 ? weight * (weight - 2.0) / (weight * weight - 3.0 * weight + 1.0) : 0.0;
+    }
+    return weight > 0.0 ? adjust * (-sum * sum) / weight : 0.0;
+}
+
 /* multi_dim_split_score_into at dim 1 (score.rs:192-265): `ld`/`lw` hold the
  * 2P canonical-order leaves (false children 0..P-1, then true children). */
 static double split_score(int32_t score_fn, const double* ld, const double* lw, int32_t nleaves,
                           double l2) {
+    if (score_fn > ORC_SCORE_L2) {
+        double acc = 0.0;
+        for (int32_t k = 0; k < nleaves; ++k) acc += orc_score_term(score_fn, ld[k], lw[k]);
+        return acc;
+    }
     double num = 0.0;
     for (int32_t k = 0; k < nleaves; ++k) {
         double avg = calc_average(ld[k], lw[k], l2);

@@ -108,7 +108,11 @@ void orc_build_histogram(const uint8_t* bins_fm, int64_t n, int32_t F, int32_t n
                          int32_t n_leaves, double* out_hist);
 
 /* ---- the boosting loop (crates/cb-train/src/boosting.rs CPU branch) ---- */
-enum { ORC_SCORE_COSINE = 0, ORC_SCORE_L2 = 1 };
+enum { ORC_SCORE_COSINE = 0, ORC_SCORE_L2 = 1, ORC_SCORE_SOLAR_L2 = 2, ORC_SCORE_LOO_L2 = 5, ORC_SCORE_SAT_L2 = 6 };
+
+/* The per-leaf terms of SolarL2 / LOOL2 / SatL2 (score.rs:266-330): the
+ * score is their sum in dimension-then-leaf order, without l2. */
+double orc_score_term(int32_t score_fn, double sum, double weight);
 
 typedef struct {
     int64_t n;

@@ -125,6 +125,12 @@ void orc_solve_symmetric_newton(const double* sum_der, const double* sum_der2_pa
 /* multi_dim_split_score_into (score.rs:192-265): ld[d * nl + leaf], lw[leaf]. */
 static double mc_split_score(int32_t score_fn, const double* ld, const double* lw, int32_t K, int32_t nl,
                              double l2) {
+    if (score_fn > ORC_SCORE_L2) { /* SolarL2 / LOOL2 / SatL2 */
+        double acc = 0.0;
+        for (int32_t d = 0; d < K; ++d)
+            for (int32_t q = 0; q < nl; ++q) acc += orc_score_term(score_fn, ld[d * nl + q], lw[q]);
+        return acc;
+    }
     double num = 0.0;
     for (int32_t d = 0; d < K; ++d)
         for (int32_t q = 0; q < nl; ++q) {

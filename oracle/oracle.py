@@ -19,7 +19,7 @@ _lib = None
 
 LOSS = {"RMSE": 0, "Logloss": 1, "CrossEntropy": 2}
 BOOT = {"No": 0, "Bayesian": 1, "Bernoulli": 2, "MVS": 3}
-SCORE = {"Cosine": 0, "L2": 1}
+SCORE = {"Cosine": 0, "L2": 1, "SolarL2": 2, "LOOL2": 5, "SatL2": 6}
 BORDER_TYPE = {"Median": 0, "GreedyLogSum": 1, "UniformAndQuantiles": 2, "MinEntropy": 3,
                "MaxLogSum": 4, "Uniform": 5, "GreedyMinEntropy": 6}
 NAN_MODE = {"Min": 0, "Max": 1, "Forbidden": 2}
@@ -138,6 +138,8 @@ def lib():
         L.orc_train_multiclass.argtypes = [P(_MultiArgs), P(_MultiOut)]
         L.orc_train_multiclass.restype = C.c_int
         L.orc_solve_symmetric_newton.argtypes = [C.c_void_p, C.c_void_p, C.c_int32, C.c_double, C.c_void_p]
+        L.orc_score_term.argtypes = [C.c_int32, C.c_double, C.c_double]
+        L.orc_score_term.restype = C.c_double
         L.orc_cat_hash.argtypes = [C.c_char_p, C.c_size_t]
         L.orc_cat_hash.restype = C.c_uint32
         L.orc_city_hash64.argtypes = [C.c_char_p, C.c_size_t]
@@ -501,3 +503,8 @@ def perfect_hash_bins(values) -> tuple:
     for i, v in enumerate(values):
         out[i] = index.setdefault(v, len(index))
     return out, list(index)
+
+
+def score_term(score_function: str, sum_der: float, weight: float) -> float:
+    """One leaf's SolarL2 / LOOL2 / SatL2 score term (score.rs:266-330)."""
+    return lib().orc_score_term(SCORE[score_function], sum_der, weight)

@@ -68,6 +68,8 @@ CASES = [
     dict(n=30000, F=20, K=10, depth=6, boot="Bernoulli", score="Cosine", it=5),
     dict(n=20000, F=15, K=5, depth=5, boot="Bayesian", score="L2", it=5),
     dict(n=70001, F=6, K=4, depth=8, boot="No", score="Cosine", it=3),
+    dict(n=6000, F=8, K=4, depth=4, boot="No", score="SolarL2", it=4),
+    dict(n=6000, F=8, K=3, depth=4, boot="Bernoulli", score="SatL2", it=4),
 ]
 
 

@@ -196,6 +196,30 @@ def test_device_fit_matches_oracle(case):
     assert np.max(np.abs(m.staged - o.staged)) <= PRED_TOL
 
 
+@pytest.mark.parametrize("score", ["SolarL2", "LOOL2", "SatL2"])
+@pytest.mark.parametrize("loss,boot", [("RMSE", "No"), ("Logloss", "Bayesian")])
+def test_device_fit_other_score_functions(score, loss, boot):
+    # SolarL2 / LOOL2 / SatL2 (crates/cb-compute/src/score.rs:245-330): the
+    # sum of per-leaf terms over the same histograms, no l2.  A level that
+    # repeats one of the tree's earlier splits leaves every partition as it
+    # was; all such candidates tie exactly and rounding picks among them, so
+    # those levels are compared through the predictions only.
+    X, y, borders = make_dataset(4000, 14, seed=17, nan_frac=0.02, loss=loss, border_count=32)
+    fp = cb.FitParams(loss=loss, depth=5, iterations=5, learning_rate=0.1, l2_leaf_reg=3.0, score_function=score,
+                      bootstrap_type=boot, bagging_temperature=1.0, random_seed=3,
+                      boost_from_average=loss == "RMSE")
+    m = cb.fit(_cols(X), borders, y, fp, staged=True)
+    o = _oracle_fit(X, y, borders, fp)
+    for t in range(fp.iterations):
+        for l in range(fp.depth):
+            a = (m.split_feature[t, l], m.split_bin[t, l])
+            b = (o.split_feature[t, l], o.split_bin[t, l])
+            seen_m = set(zip(m.split_feature[t, :l], m.split_bin[t, :l]))
+            seen_o = set(zip(o.split_feature[t, :l], o.split_bin[t, :l]))
+            assert a == b or (a in seen_m and b in seen_o), (t, l)
+    assert np.max(np.abs(m.staged - o.staged)) <= PRED_TOL
+
+
 def test_weighted_fit_matches_oracle():
     X, y, borders = make_dataset(6000, 16, seed=9, border_count=32)
     w = np.random.RandomState(2).choice([0.5, 1.0, 2.0, 3.0], size=X.shape[0])
