@@ -196,7 +196,7 @@ def test_multiclass_caller_approx_and_declines(cb):
                                           borders, None, n, F, nb, 0.1, 3.0, cfg, approx_dim=kw.pop("K", K))
         return rt, ok
 
-    for kw in (dict(boot="MVS"), dict(K=1), dict(K=17), dict(loss="RMSE"), dict(score="SolarL2")):
+    for kw in (dict(boot="MVS"), dict(K=1), dict(K=17), dict(loss="RMSE"), dict(score="NewtonL2")):
         rt, ok = begin(**kw)
         assert not ok and rt.decline_reason, kw
     rt, ok = begin()

@@ -315,7 +315,8 @@ def test_begin_u32_bins_path_matches_raw_path():
     ref = cb.fit(_cols(X), borders, y, fp, staged=True)
     rt = cb.B200Runtime()
     cfg = cb.DeviceTrainConfig(bias=ref.bias, border_counts=[len(b) for b in borders])
-    assert rt.begin_device_training("RMSE", 4, True, 1, "L2", bins, None, 4000, 9, nb, 0.1, 3.0, cfg)
+    lr = float(np.float32(fp.learning_rate))  # fit hands the seam the f32-narrowed rate (boosting.rs:4958)
+    assert rt.begin_device_training("RMSE", 4, True, 1, "L2", bins, None, 4000, 9, nb, lr, 3.0, cfg)
     for it in range(3):
         tree = rt.grow_tree_on_device(None, y, [], resident_approx=True)
         assert [s[0] for s in tree.splits] == list(ref.split_feature[it])
