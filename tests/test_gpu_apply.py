@@ -125,7 +125,7 @@ def test_fit_then_predict(cb):
     n, F = 20000, 10
     X = rs.standard_normal((n, F)).astype(np.float32)
     X[rs.uniform(size=X.shape) < 0.03] = np.nan
-    y = X[:, 0] - 2 * np.nan_to_num(X[:, 1]) + 0.1 * rs.standard_normal(n)
+    y = np.nan_to_num(X[:, 0]) - 2 * np.nan_to_num(X[:, 1]) + 0.1 * rs.standard_normal(n)  # a finite target
     borders = [np.concatenate([[-FMAX], np.unique(np.quantile(X[~np.isnan(X[:, f]), f],
                                                               np.linspace(0, 1, 34)[1:-1]).astype(np.float32))
                                .astype(np.float64)]) for f in range(F)]
