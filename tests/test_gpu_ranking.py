@@ -228,6 +228,53 @@ def test_pairwise_matches_oracle(cb, depth, n_groups):
     assert np.max(np.abs(m.staged - o.staged)) <= TOL
 
 
+EDGE_LOSSES = ["QueryRMSE", "QuerySoftMax", "LambdaMart", "YetiRank", "YetiRankPairwise", "StochasticRank",
+               "PairLogit", "PairLogitPairwise"]
+
+
+@pytest.mark.parametrize("loss", EDGE_LOSSES)
+def test_ranking_edge_groups(cb, loss):
+    # singleton groups, two-document groups, groups of equal relevance and
+    # documents without pairs, against the oracle
+    rs = np.random.RandomState(77)
+    sizes = [1, 2, 1, 5, 1, 3, 7, 2, 1, 4, 6, 1, 8, 3]
+    offsets = np.concatenate([[0], np.cumsum(sizes)]).astype(np.int64)
+    n, F = int(offsets[-1]), 4
+    X = rs.standard_normal((n, F)).astype(np.float32)
+    y = rs.randint(0, 4, n).astype(np.float64)
+    y[offsets[3]:offsets[4]] = 2.0  # a group of equal relevance
+    pairs = []
+    for g in range(len(sizes)):
+        b, e = offsets[g], offsets[g + 1]
+        for i in range(b, e):
+            for j in range(b, e):
+                if y[i] > y[j] and rs.uniform() < 0.7:
+                    pairs.append((i, j))
+    pairs = np.array(pairs, dtype=np.int64).reshape(-1, 2)
+    borders = [oracle.select_borders(X[:, f], 8) for f in range(F)]
+    fp = cb.FitParams(loss=loss, depth=3, iterations=3, learning_rate=0.3, l2_leaf_reg=2.0, random_seed=3,
+                      boost_from_average=False, yeti_permutations=3)
+    m = cb.fit_ranking([X[:, f].copy() for f in range(F)], borders, y, offsets, fp, pairs=pairs, staged=True)
+    bins = oracle.quantize(X.T.copy(), borders)
+    o = oracle.train_ranking(bins, [len(b) for b in borders], y, offsets, loss=loss, pairs=pairs, depth=3,
+                             iterations=3, learning_rate=0.3, l2_leaf_reg=2.0, random_seed=3, yeti_permutations=3)
+    np.testing.assert_array_equal(m.split_feature, o.split_feature)
+    np.testing.assert_array_equal(m.split_bin, o.split_bin)
+    assert np.max(np.abs(m.leaf_values - o.leaf_values)) <= TOL
+    assert np.max(np.abs(m.staged - o.staged)) <= TOL
+
+
+def test_pair_losses_without_pairs(cb):
+    # PairLogit with an empty pair list: zero ders everywhere, zero leaves
+    X, y, offsets, _ = _ranking_data(10, 4, 5)
+    F = X.shape[1]
+    borders = [oracle.select_borders(X[:, f], 8) for f in range(F)]
+    fp = cb.FitParams(loss="PairLogit", depth=2, iterations=2, learning_rate=0.3, boost_from_average=False)
+    m = cb.fit_ranking([X[:, f].copy() for f in range(F)], borders, y, offsets, fp,
+                       pairs=np.zeros((0, 2), dtype=np.int64), staged=True)
+    assert np.all(m.leaf_values == 0.0) and np.all(m.staged == 0.0)
+
+
 def test_ranking_declines_and_errors(cb):
     from catboost_rs_b200 import CbGpuError
     X, y, offsets, pairs = _ranking_data(20, 4, 3)
