@@ -143,6 +143,36 @@ def test_multiclass_one_hot_declines_bootstrap(cb):
                           cat_columns=[[str(i % 300) for i in range(n)]])
 
 
+@pytest.mark.parametrize("case", ["depth1", "absent_class", "zero_weights", "constant_feature"])
+def test_multiclass_edges(cb, case):
+    # depth 1, a class no row carries, zero-weight rows, a feature without borders
+    rs = np.random.RandomState(21)
+    n, F, K = 3000, 5, 4
+    X = rs.standard_normal((n, F)).astype(np.float32)
+    cls = np.argmax(X[:, :K] + rs.gumbel(size=(n, K)), axis=1).astype(np.int32)
+    w = None
+    depth = 4
+    if case == "depth1":
+        depth = 1
+    elif case == "absent_class":
+        cls[cls == 2] = 1
+    elif case == "zero_weights":
+        w = rs.choice([0.0, 1.0, 3.0], size=n)
+    borders = [oracle.select_borders(X[:, f], 16) for f in range(F)]
+    if case == "constant_feature":
+        X[:, 2] = 0.5
+        borders[2] = np.zeros(0)
+    fp = _fp(cb, depth=depth, iterations=3)
+    m = cb.fit_multiclass([X[:, f].copy() for f in range(F)], borders, cls, K, fp, weights=w, staged=True)
+    bins = oracle.quantize(X.T.copy(), borders)
+    o = oracle.train_multiclass(bins, [len(b) for b in borders], cls, K, depth=depth, iterations=3,
+                                learning_rate=fp.learning_rate, l2_leaf_reg=fp.l2_leaf_reg, weights=w)
+    np.testing.assert_array_equal(m.split_feature, o.split_feature)
+    np.testing.assert_array_equal(m.split_bin, o.split_bin)
+    assert np.max(np.abs(m.leaf_values - o.leaf_values)) <= TOL
+    assert np.max(np.abs(m.staged - o.staged)) <= TOL
+
+
 def test_multiclass_host_sample_and_run_twice(cb):
     rs = np.random.RandomState(2)
     n, F, K = 8000, 6, 3
