@@ -402,6 +402,7 @@ int orc_train_multiclass(const orc_multi_args* a, orc_multi_out* o) {
     double* approx = (double*)calloc(nk + 1, sizeof(double)); /* [K][n], bias 0 */
     double* wd1 = (double*)malloc(sizeof(double) * (nk + 1));  /* [K][n] */
     double* d2p = (double*)malloc(sizeof(double) * ((size_t)n * pk + 1));
+    const int diag = a->loss_kind == 1;
     double* sg = (double*)malloc(sizeof(double) * (nk + 1));
     double* sh = (double*)malloc(sizeof(double) * ((size_t)n + 1));
     double* dobj = (double*)malloc(sizeof(double) * ((size_t)n + 1));
@@ -421,6 +422,19 @@ int orc_train_multiclass(const orc_multi_args* a, orc_multi_out* o) {
     int rc = 0;
     for (int32_t it = 0; it < a->iterations; ++it) {
         for (int64_t i = 0; i < n; ++i) {
+            if (diag) {
+                /* multiclass_onevsall_ders / multi_crossentropy_ders (loss.rs:501-560):
+                 * per dimension p = sigmoid(a_d), der1 = t_d - p, der2 = -p (1 - p) */
+                for (int32_t d = 0; d < K; ++d) {
+                    const double av = approx[(size_t)d * n + i];
+                    const double p = 1.0 - 1.0 / (1.0 + exp(av));
+                    const double t = a->target_matrix[(size_t)d * n + i];
+                    wd1[(size_t)d * n + i] = (t - p) * w[i];
+                    d2p[(size_t)i * pk + d] = -p * (1.0 - p);
+                }
+                for (int32_t j = K; j < pk; ++j) d2p[(size_t)i * pk + j] = 0.0;
+                continue;
+            }
             for (int32_t d = 0; d < K; ++d) pa[d] = approx[(size_t)d * n + i];
             softmax_ders(pa, K, a->target_class[i], pp, p1, p2);
             for (int32_t d = 0; d < K; ++d) wd1[(size_t)d * n + i] = p1[d] * w[i];
@@ -468,7 +482,14 @@ int orc_train_multiclass(const orc_multi_args* a, orc_multi_out* o) {
         for (int32_t k = 0; k < K * L; ++k) lvd[k] = 0.0;
         for (int32_t q = 0; q < nl; ++q) {
             const double* s = ls + (size_t)q * (K + pk);
-            orc_solve_symmetric_newton(s, s + K, K, scaled_l2, pp);
+            if (diag) { /* newton_leaf_delta per dimension (leaf.rs:196-232) */
+                for (int32_t d = 0; d < K; ++d) {
+                    const double den = -s[K + d] + scaled_l2;
+                    pp[d] = den == 0.0 ? 0.0 : s[d] / den;
+                }
+            } else {
+                orc_solve_symmetric_newton(s, s + K, K, scaled_l2, pp);
+            }
             for (int32_t d = 0; d < K; ++d) lvd[(size_t)d * L + q] = pp[d] * lr; /* normalize_leaf_values */
         }
         double* out_lv = o->leaf_values + (size_t)it * L * K; /* leaf-major */

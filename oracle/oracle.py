@@ -66,6 +66,7 @@ class _MultiArgs(C.Structure):
         ("learning_rate", C.c_double), ("l2_leaf_reg", C.c_double), ("score_function", C.c_int32),
         ("bootstrap_type", C.c_int32), ("subsample", C.c_double), ("bagging_temperature", C.c_float),
         ("random_seed", C.c_uint64), ("n_threads", C.c_int32), ("n_cat", C.c_int32), ("cat_bins_fm", C.c_void_p),
+        ("loss_kind", C.c_int32), ("target_matrix", C.c_void_p),
     ]
 
 
@@ -374,18 +375,36 @@ class OracleMultiFit:
     final_approx: np.ndarray   # [n, K]
 
 
+MULTI_LOSSES = ("MultiClass", "MultiClassOneVsAll", "MultiLogloss", "MultiCrossEntropy")
+
+
 def train_multiclass(bins_fm, border_counts, target_class, n_classes, *, depth=6, iterations=10,
                      learning_rate=0.1, l2_leaf_reg=3.0, score_function="Cosine", bootstrap_type="No",
                      subsample=0.66, bagging_temperature=1.0, random_seed=0, weights=None, staged=True,
-                     n_threads=0, cat_bins_fm=None) -> OracleMultiFit:
-    """The reference's MultiClass (softmax, Newton leaves) CPU loop on quantized bins;
-    cat_bins_fm [C, n] adds one-hot categorical features (split_feature >= F)."""
+                     n_threads=0, cat_bins_fm=None, loss="MultiClass") -> OracleMultiFit:
+    """The reference's multi-output CPU loop on quantized bins, Newton leaves.
+
+    loss "MultiClass" (softmax, dense Hessian solve) and "MultiClassOneVsAll"
+    take class indices in target_class; "MultiLogloss" and "MultiCrossEntropy"
+    take a [K, n] label matrix (dim-major), all three diagonal losses solving
+    each dimension on its own (boosting.rs:8323-8420).  cat_bins_fm [C, n] adds
+    one-hot categorical features (split_feature >= F)."""
     bins = np.ascontiguousarray(bins_fm, dtype=np.uint8)
     F, n = bins.shape
     cb = None if cat_bins_fm is None else np.ascontiguousarray(cat_bins_fm, dtype=np.uint8).reshape(-1, n)
     K = int(n_classes)
     bc = np.ascontiguousarray(border_counts, dtype=np.int32)
-    y = np.ascontiguousarray(target_class, dtype=np.int32)
+    if loss not in MULTI_LOSSES:
+        raise ValueError(f"unknown multi-output loss {loss}")
+    tm = None
+    if loss == "MultiClass":
+        y = np.ascontiguousarray(target_class, dtype=np.int32)
+    elif loss == "MultiClassOneVsAll":
+        y = np.ascontiguousarray(target_class, dtype=np.int32)
+        tm = np.ascontiguousarray((np.arange(K)[:, None] == y[None, :]).astype(np.float64))
+    else:
+        tm = np.ascontiguousarray(target_class, dtype=np.float64).reshape(K, n)
+        y = None
     w = None if weights is None else np.ascontiguousarray(weights, dtype=np.float64)
     L = 1 << depth
     sf = np.empty((iterations, depth), dtype=np.int32)
@@ -396,7 +415,7 @@ def train_multiclass(bins_fm, border_counts, target_class, n_classes, *, depth=6
     fa = np.empty((n, K), dtype=np.float64)
     args = _MultiArgs(n, F, _p(bins), _p(bc), _p(y), _p(w), K, depth, iterations, learning_rate, l2_leaf_reg,
                       SCORE[score_function], BOOT[bootstrap_type], subsample, bagging_temperature, random_seed,
-                      n_threads, 0 if cb is None else cb.shape[0], _p(cb))
+                      n_threads, 0 if cb is None else cb.shape[0], _p(cb), 0 if tm is None else 1, _p(tm))
     out = _MultiOut(_p(sf), _p(sb), _p(td), _p(lv), _p(st), _p(fa))
     rc = lib().orc_train_multiclass(C.byref(args), C.byref(out))
     if rc != 0:

@@ -233,6 +233,49 @@ def multiclass_fixture(ref):
     return "multiclass_softmax"
 
 
+def multi_output_fixtures(ref):
+    """Upstream MultiClassOneVsAll, MultiLogloss and MultiCrossEntropy fixtures
+    on numeric_tiny (Newton leaves, depth 2, 5 iterations).  Labels are stored
+    as the dim-major [K, n] matrix each fit consumes: OneVsAll's one-hot of the
+    digitized classes (the multiclass_softmax rule); for the two label losses
+    the nested thresholds y > quantile(y, [.25, .5, .75]) that the reference's
+    multilabel_oracle_test.rs:67-85 derives (the configs' target_rule text
+    names another rule, which does not reproduce upstream's staged values)."""
+    fx = os.path.join(ref, "crates/cb-oracle/fixtures")
+    X = np.load(os.path.join(fx, "inputs/numeric_tiny/X.npy"))
+    y = np.load(os.path.join(fx, "inputs/numeric_tiny/y.npy"))
+    n = X.shape[0]
+    out = {"X": X.astype(np.float32)}
+    for sc in ("multiclass_onevsall", "multilogloss", "multicrossentropy"):
+        cfg = json.loads(_read(os.path.join(fx, sc, "config.json")))
+        model = json.loads(_read(os.path.join(fx, sc, "model.json")))
+        K = int(cfg["approx_dimension"])
+        if sc == "multiclass_onevsall":
+            cls = np.digitize(y, np.quantile(y, [1 / 3, 2 / 3]))
+            labels = (np.arange(K)[:, None] == cls[None, :]).astype(np.float64)
+        else:
+            labels = np.vstack([y > np.quantile(y, q) for q in (0.25, 0.5, 0.75)]).astype(np.float64)
+        trees = model["oblivious_trees"]
+        depth = max(len(t["splits"]) for t in trees)
+        p = cfg["params"]
+        params = {"loss": cfg["loss_function"], "approx_dimension": K, "depth": int(p["depth"]),
+                  "iterations": int(p["iterations"]), "learning_rate": float(p["learning_rate"]),
+                  "l2_leaf_reg": float(p["l2_leaf_reg"]), "score_function": p["score_function"],
+                  "leaf_estimation_method": p["leaf_estimation_method"], "border_count": 254,
+                  "border_type": "GreedyLogSum"}
+        out[f"{sc}__labels"] = labels
+        out[f"{sc}__split_feature"] = np.array([[s["float_feature_index"] for s in t["splits"]] for t in trees],
+                                               dtype=np.int32)
+        out[f"{sc}__split_border"] = np.array([[s["border"] for s in t["splits"]] for t in trees], dtype=np.float64)
+        out[f"{sc}__leaf_values"] = np.array([t["leaf_values"] for t in trees],
+                                             dtype=np.float64).reshape(len(trees), 1 << depth, K)
+        out[f"{sc}__staged"] = np.load(os.path.join(fx, sc, "staged.npy")).reshape(len(trees), n, K)
+        out[f"{sc}__probabilities"] = np.load(os.path.join(fx, sc, "predictions.npy")).reshape(n, K)
+        out[f"{sc}__params"] = np.array(json.dumps(params))
+    np.savez_compressed(os.path.join(OUT, "multi_output.npz"), **out)
+    return "multi_output"
+
+
 def ranking_fixtures(ref):
     """Upstream QueryRMSE / PairLogit / PairLogitPairwise / QuerySoftMax / LambdaMart fixtures on the reference's frozen ranking
     corpus (12 objects, 5 contiguous groups, 7 explicit pairs): inputs, group
@@ -373,6 +416,7 @@ def main():
     border_cells = border_fixtures(ref)
     written = e2e_fixtures(ref)
     written.append(multiclass_fixture(ref))
+    written.append(multi_output_fixtures(ref))
     written += ranking_fixtures(ref)
     written += one_hot_fixtures(ref)
     written += model_json_fixtures(ref)
