@@ -185,12 +185,19 @@ def perfect_hash_bins(column):
 
 def fit_multiclass(float_columns: Sequence[np.ndarray], borders: Sequence[Sequence[float]], target_class,
                    n_classes: int, params: FitParams, weights=None, *, staged: bool = False,
-                   device: int = 0, cat_columns=None) -> MultiClassModel:
-    """MultiClass (softmax, Newton leaves) fit on raw f32 columns with fixed
-    borders: cb-train's multi-output loop (boosting.rs:7400-8930 at
-    approx_dimension K) over the device's multi-output arm.  cat_columns are
-    one-hot categorical features (any hashable values; bins in first-seen
-    order); they need bootstrap No, as upstream."""
+                   device: int = 0, cat_columns=None, loss: str = "MultiClass") -> MultiClassModel:
+    """Multi-output fit (Newton leaves) on raw f32 columns with fixed borders:
+    cb-train's multi-output loop (boosting.rs:7400-8930 at approx_dimension K)
+    over the device's multi-output arm.
+
+    loss "MultiClass" (softmax, coupled Hessian solve) and "MultiClassOneVsAll"
+    (per-class sigmoid) take class indices in target_class; "MultiLogloss"
+    ({0, 1}) and "MultiCrossEntropy" ([0, 1]) take the [K, n] label matrix
+    (dim-major, the reference's multilabel layout) with n_classes = K labels.
+    The three diagonal losses solve each dimension's leaf on its own
+    (boosting.rs:8323-8420).  cat_columns are one-hot categorical features
+    (any hashable values; bins in first-seen order); they need bootstrap No,
+    as upstream."""
     p = params
     cols = [np.ascontiguousarray(c, dtype=np.float32) for c in float_columns]
     F = len(cols)
@@ -211,7 +218,7 @@ def fit_multiclass(float_columns: Sequence[np.ndarray], borders: Sequence[Sequen
         b, v = perfect_hash_bins(col)
         cat_bins.append(b)
         cat_values.append(v)
-    ok = rt.begin_device_training_raw("MultiClass", p.depth, True, 1, p.score_function, cols, borders, w, n, F,
+    ok = rt.begin_device_training_raw(loss, p.depth, True, 1, p.score_function, cols, borders, w, n, F,
                                       n_bins, lr, scaled_l2, cfg, approx_dim=K, cat_columns=cat_bins)
     if not ok:
         raise RuntimeError(f"device declined: {rt.decline_reason}")

@@ -137,11 +137,19 @@ __device__ __forceinline__ void mc_softmax(const double* __restrict__ approx, in
     for (int d = 0; d < K; ++d) p[d] = __ddiv_rn(p[d], s);
 }
 
-// approx += lr * leaf (the previous tree, when pending); wd1[d] = ([d == y] - p[d]) * w.
+// sigmoid (loss.rs:54-57): 1 - 1 / (1 + exp(a)).
+__device__ __forceinline__ double mc_sigmoid(double a) {
+    return __dsub_rn(1.0, __ddiv_rn(1.0, __dadd_rn(1.0, exp(a))));
+}
+
+// approx += lr * leaf (the previous tree, when pending); then the weighted der1
+// per dimension: softmax wd1[d] = ([d == y] - p[d]) * w; diagonal (loss.rs:501-560)
+// wd1[d] = (t_d - sigmoid(a_d)) * w with t_d = tmat[d * n + i], or [d == y]
+// without a label matrix (MultiClassOneVsAll).
 __global__ void mc_der_kernel(int64_t n, int K, double* __restrict__ approx, const int32_t* __restrict__ target,
                               const double* __restrict__ weight, const uint16_t* __restrict__ leaf,
-                              const double* __restrict__ lrv, int L, int pending, double* __restrict__ wd1,
-                              McState* __restrict__ ms) {
+                              const double* __restrict__ lrv, int L, int pending, int diag,
+                              const double* __restrict__ tmat, double* __restrict__ wd1, McState* __restrict__ ms) {
     double p[kMcMaxK];
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
         if (pending) {
@@ -149,10 +157,21 @@ __global__ void mc_der_kernel(int64_t n, int K, double* __restrict__ approx, con
             for (int d = 0; d < K; ++d)
                 approx[(size_t)d * n + i] = __dadd_rn(approx[(size_t)d * n + i], lrv[(size_t)d * L + q]);
         }
-        mc_softmax(approx, n, i, K, p);
         const double w = weight ? weight[i] : 1.0;
-        const int y = target[i];
         bool finite = true;
+        if (diag) {
+            const int y = tmat ? -1 : target[i];
+            for (int d = 0; d < K; ++d) {
+                const double t = tmat ? tmat[(size_t)d * n + i] : (d == y ? 1.0 : 0.0);
+                const double v = __dmul_rn(__dsub_rn(t, mc_sigmoid(approx[(size_t)d * n + i])), w);
+                finite &= isfinite(v);
+                wd1[(size_t)d * n + i] = v;
+            }
+            if (!finite) atomicOr(&ms->err, kMcErrNonFinite);
+            continue;
+        }
+        mc_softmax(approx, n, i, K, p);
+        const int y = target[i];
         for (int d = 0; d < K; ++d) {
             double d1 = -p[d];
             if (d == y) d1 = __dadd_rn(d1, 1.0);
@@ -383,10 +402,12 @@ __global__ void mc_route_kernel(int64_t n, int level, const uint8_t* __restrict_
 
 // Per-leaf sums of w*der1[d] (K) and w*der2 packed (pk) over ALL rows
 // (compute_softmax_leaf_deltas, boosting.rs:2610-2700), int64 fixed point at
-// 2^leaf_shift; table[L][K + pk] in shared memory when it fits.
+// 2^leaf_shift; table[L][K + pk] in shared memory when it fits.  Diagonal
+// losses fill only the first K der2 slots: w * (-p_d (1 - p_d)) per dimension
+// (the per-dimension scalar sums of boosting.rs:8323-8420).
 __global__ void __launch_bounds__(kMcThreads)
 mc_leafsum_kernel(int64_t n, int K, int L, const double* __restrict__ approx, const double* __restrict__ wd1,
-                  const double* __restrict__ weight, const uint16_t* __restrict__ leaf, int leaf_shift,
+                  const double* __restrict__ weight, const uint16_t* __restrict__ leaf, int leaf_shift, int diag,
                   unsigned long long* __restrict__ sums, int use_smem, McState* __restrict__ ms) {
     extern __shared__ unsigned long long ltab[];
     const int pk = K * (K + 1) / 2, W = K + pk;
@@ -405,8 +426,16 @@ mc_leafsum_kernel(int64_t n, int K, int L, const double* __restrict__ approx, co
         unsigned long long* cell = dst + (size_t)q * W;
         for (int d = 0; d < K; ++d)
             atomicAdd(&cell[d], (unsigned long long)llrint(ldexp(wd1[(size_t)d * n + i], leaf_shift)));
-        mc_softmax(approx, n, i, K, p);
         const double w = weight ? weight[i] : 1.0;
+        if (diag) {
+            for (int d = 0; d < K; ++d) {
+                const double pd = mc_sigmoid(approx[(size_t)d * n + i]);
+                const double h = __dmul_rn(__dmul_rn(-pd, __dsub_rn(1.0, pd)), w);
+                atomicAdd(&cell[K + d], (unsigned long long)llrint(ldexp(h, leaf_shift)));
+            }
+            continue;
+        }
+        mc_softmax(approx, n, i, K, p);
         int j = 0;
         for (int dy = 0; dy < K; ++dy) {
             const double hyy = __dmul_rn(__dmul_rn(p[dy], __dsub_rn(p[dy], 1.0)), w);
@@ -427,12 +456,27 @@ mc_leafsum_kernel(int64_t n, int K, int L, const double* __restrict__ approx, co
 // solve_symmetric_newton (leaf.rs:281-340) for leaf `threadIdx.x`: Rust
 // f32::max semantics for the trace regulariser, Cholesky (leaf.rs:360-420),
 // zeros on a non-positive pivot; delta x lr for the approximant.
+// Diagonal losses: newton_leaf_delta per dimension (leaf.rs:196-232),
+// s1 / (-s2 + l2), 0 on a zero denominator.
 __global__ void mc_newton_kernel(int K, int L, const unsigned long long* __restrict__ sums, int leaf_shift,
-                                 double l2, double lr, double* __restrict__ leaf_raw, double* __restrict__ leaf_lrv) {
+                                 double l2, double lr, int diag, double* __restrict__ leaf_raw,
+                                 double* __restrict__ leaf_lrv) {
     const int q = blockIdx.x * blockDim.x + threadIdx.x;
     if (q >= L) return;
     const int pk = K * (K + 1) / 2, W = K + pk;
     const double inv = ldexp(1.0, -leaf_shift);
+    if (diag) {
+        const unsigned long long* s = sums + (size_t)q * W;
+        for (int d = 0; d < K; ++d) {
+            const double s1 = __dmul_rn((double)(long long)s[d], inv);
+            const double s2 = __dmul_rn((double)(long long)s[K + d], inv);
+            const double den = __dadd_rn(-s2, l2);
+            const double delta = den == 0.0 ? 0.0 : __ddiv_rn(s1, den);
+            leaf_raw[(size_t)q * K + d] = delta;
+            leaf_lrv[(size_t)d * L + q] = __dmul_rn(delta, lr);
+        }
+        return;
+    }
     double H[kMcMaxK * kMcMaxK], Lm[kMcMaxK * kMcMaxK], y[kMcMaxK], x[kMcMaxK], g[kMcMaxK];
     const unsigned long long* s = sums + (size_t)q * W;
     for (int d = 0; d < K; ++d) g[d] = __dmul_rn((double)(long long)s[d], inv);
@@ -1384,6 +1428,9 @@ unsigned grid_for(int64_t n, int threads = kMcThreads) {
 struct cbgpu_multi_session {
     int device = 0, K = 0, depth = 0, F = 0, NB = 0, score_fn = 0, boot = 0, sample_from_host = 0;
     int F0 = 0;                    // float features; F0..F-1 are one-hot categorical
+    int loss = 0;                  // cbgpu_loss of a multi-output session
+    int diag = 0;                  // 1: the diagonal losses (OneVsAll, MultiLogloss, MultiCrossEntropy)
+    double* d_tmat = nullptr;      // [K][n] label matrix of MultiLogloss / MultiCrossEntropy
     uint8_t* d_present = nullptr;  // [F - F0][NB] learn-set bins of each categorical feature
     float sample_rate = 1.0f, temp = 1.0f;
     double lr = 0.0, l2 = 0.0;
@@ -1448,6 +1495,7 @@ struct cbgpu_multi_session {
     ~cbgpu_multi_session() {
         if (st) cudaStreamSynchronize(st);
         cudaFree(d_srank_ws);
+        cudaFree(d_tmat);
         cudaFree(d_present);
         cudaFree(d_gw);
         cudaFree(d_yseeds);
@@ -1529,6 +1577,9 @@ int begin_impl(const cbgpu_begin_args* a, int32_t K, const float* const* cols, c
     s->depth = a->depth;
     s->F0 = a->n_features;
     s->F = a->n_features + n_cat;
+    s->loss = a->loss;
+    s->diag = a->loss == CBGPU_LOSS_MULTICLASS_ONE_VS_ALL || a->loss == CBGPU_LOSS_MULTILOGLOSS ||
+              a->loss == CBGPU_LOSS_MULTICROSSENTROPY;
     s->score_fn = a->score_function;
     s->boot = a->bootstrap_type;
     s->sample_from_host = a->sample_from_host;
@@ -1575,6 +1626,7 @@ int begin_impl(const cbgpu_begin_args* a, int32_t K, const float* const* cols, c
     MDA(s->wd1, (size_t)K * n);
     MDA(s->q, (size_t)C * n);
     MDA(s->target, n);
+    if (a->loss == CBGPU_LOSS_MULTILOGLOSS || a->loss == CBGPU_LOSS_MULTICROSSENTROPY) MDA(s->d_tmat, (size_t)K * n);
     MDA(s->leaf, n);
     MDA(s->sw32, n);
     MDA(s->sw64, n);
@@ -1665,7 +1717,9 @@ int cbgpu_multi_begin_cat_raw(const cbgpu_begin_args* a, int32_t approx_dim, con
             return mfail(CBGPU_DECLINED, "multi_begin: one-hot categorical features need bootstrap No");
     }
     // the coverage this arm accepts; everything else declines to the CPU grower
-    if (a->loss != CBGPU_LOSS_MULTICLASS) return mfail(CBGPU_DECLINED, "multi_begin: loss is not MultiClass");
+    const bool labels = a->loss == CBGPU_LOSS_MULTILOGLOSS || a->loss == CBGPU_LOSS_MULTICROSSENTROPY;
+    if (a->loss != CBGPU_LOSS_MULTICLASS && a->loss != CBGPU_LOSS_MULTICLASS_ONE_VS_ALL && !labels)
+        return mfail(CBGPU_DECLINED, "multi_begin: loss %d is not a covered multi-output loss", a->loss);
     if (a->grow_policy != CBGPU_GROW_SYMMETRIC || !a->boosting_type_is_plain || a->fold_count != 1)
         return mfail(CBGPU_DECLINED, "multi_begin: only Plain SymmetricTree with one fold");
     if (a->score_function != CBGPU_SCORE_COSINE && a->score_function != CBGPU_SCORE_L2 &&
@@ -1676,8 +1730,9 @@ int cbgpu_multi_begin_cat_raw(const cbgpu_begin_args* a, int32_t approx_dim, con
     if (a->bootstrap_type == CBGPU_BOOT_MVS || a->bootstrap_type == CBGPU_BOOT_POISSON)
         return mfail(CBGPU_DECLINED, "multi_begin: MVS / Poisson not covered on this arm");
     if (a->world_size != 1) return mfail(CBGPU_DECLINED, "multi_begin: one GPU per multi-output session");
-    if (approx_dim < 2 || approx_dim > kMcMaxK)
-        return mfail(CBGPU_DECLINED, "multi_begin: approx_dim %d outside 2..%d", approx_dim, kMcMaxK);
+    if (approx_dim < (labels ? 1 : 2) || approx_dim > kMcMaxK)
+        return mfail(CBGPU_DECLINED, "multi_begin: approx_dim %d outside %d..%d", approx_dim, labels ? 1 : 2,
+                     kMcMaxK);
     if (a->depth < 1 || a->depth > kMcMaxDepth)
         return mfail(CBGPU_DECLINED, "multi_begin: depth %d outside 1..%d", a->depth, kMcMaxDepth);
     // histogram grids index row chunks in gridDim.z (at most 65535 chunks)
@@ -2038,6 +2093,20 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
         MCU(cudaStreamSynchronize(st));
         s->target_ready = true;
     }
+    if (!s->target_ready && s->d_tmat) {
+        // MultiLogloss {0, 1} / MultiCrossEntropy [0, 1] labels (Loss::validate)
+        if (!target) return mfail(CBGPU_ERR_INVALID, "multi_grow: the first call needs the target");
+        const bool binary = s->loss == CBGPU_LOSS_MULTILOGLOSS;
+        for (int64_t k = 0; k < (int64_t)K * n; ++k) {
+            const double t = target[k];
+            if (binary ? !(t == 0.0 || t == 1.0) : !(t >= 0.0 && t <= 1.0))
+                return mfail(CBGPU_ERR_INVALID, "multi_grow: label %g of dimension %lld row %lld is outside %s", t,
+                             (long long)(k / n), (long long)(k % n), binary ? "{0, 1}" : "[0, 1]");
+        }
+        MCU(cudaMemcpyAsync(s->d_tmat, target, sizeof(double) * (size_t)K * n, cudaMemcpyHostToDevice, st));
+        MCU(cudaStreamSynchronize(st));
+        s->target_ready = true;
+    }
     if (!s->target_ready) {
         if (!target) return mfail(CBGPU_ERR_INVALID, "multi_grow: the first call needs the target");
         std::vector<int32_t> cls((size_t)n);
@@ -2137,7 +2206,7 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
             s->wd1, s->d_der2, s->d_ms);
     } else {
         mc_der_kernel<<<g, kMcThreads, 0, st>>>(n, K, s->approx, s->target, s->weight, s->leaf, s->leaf_lrv, L,
-                                                s->pending ? 1 : 0, s->wd1, s->d_ms);
+                                                s->pending ? 1 : 0, s->diag, s->d_tmat, s->wd1, s->d_ms);
     }
     MCU(cudaGetLastError());
     s->pending = false;
@@ -2261,9 +2330,9 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
         if (luse && ltab > 48 * 1024)
             MCU(cudaFuncSetAttribute(mc_leafsum_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ltab));
         mc_leafsum_kernel<<<g, kMcThreads, luse ? ltab : 0, st>>>(n, K, L, s->approx, s->wd1, s->weight, s->leaf,
-                                                                 s->leaf_shift, s->sums, luse, s->d_ms);
-        mc_newton_kernel<<<(L + 63) / 64, 64, 0, st>>>(K, L, s->sums, s->leaf_shift, s->l2, s->lr, s->leaf_raw,
-                                                       s->leaf_lrv);
+                                                                 s->leaf_shift, s->diag, s->sums, luse, s->d_ms);
+        mc_newton_kernel<<<(L + 63) / 64, 64, 0, st>>>(K, L, s->sums, s->leaf_shift, s->l2, s->lr, s->diag,
+                                                       s->leaf_raw, s->leaf_lrv);
         MCU(cudaGetLastError());
     }
     MCU(cudaMemcpyAsync(s->h_raw, s->leaf_raw, sizeof(double) * (size_t)L * K, cudaMemcpyDeviceToHost, st));

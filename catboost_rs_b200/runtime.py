@@ -20,7 +20,10 @@ from . import _lib
 
 LOSS = {"RMSE": 0, "Rmse": 0, "Logloss": 1, "CrossEntropy": 2, "MultiClass": 3, "QueryRMSE": 4, "PairLogit": 5,
         "PairLogitPairwise": 6, "QuerySoftMax": 7,
-        "LambdaMart": 8, "YetiRank": 9, "StochasticRank": 10, "YetiRankPairwise": 11}
+        "LambdaMart": 8, "YetiRank": 9, "StochasticRank": 10, "YetiRankPairwise": 11, "MultiClassOneVsAll": 12,
+        "MultiLogloss": 13, "MultiCrossEntropy": 14}
+# multi-output losses whose target is the [K, n] label matrix (dim-major)
+LABEL_MATRIX_LOSSES = ("MultiLogloss", "MultiCrossEntropy")
 LAMBDAMART_METRIC = {"NDCG": 0, "DCG": 1, "MRR": 2, "ERR": 3, "MAP": 4}
 SCORE = {"Cosine": 0, "L2": 1, "SolarL2": 2, "NewtonL2": 3, "NewtonCosine": 4, "LOOL2": 5, "SatL2": 6}
 BOOT = {"No": 0, "Bayesian": 1, "Bernoulli": 2, "MVS": 3, "Mvs": 3, "Poisson": 4}
@@ -293,6 +296,7 @@ class B200MultiRuntime(B200Runtime):
     def __init__(self):
         super().__init__()
         self.approx_dim = 0
+        self.label_matrix = False
 
     def begin_device_training_raw(self, loss, depth, boosting_type_is_plain, fold_count, score_function,
                                   float_columns, feature_borders, weight, n, n_features, n_bins,
@@ -321,6 +325,7 @@ class B200MultiRuntime(B200Runtime):
                                                len(cats), catptrs, C.byref(self._s))
         ok = self._finish_begin(rc, n, depth)
         self.approx_dim = int(approx_dim) if ok else 0
+        self.label_matrix = ok and loss in LABEL_MATRIX_LOSSES
         return ok
 
     def begin_device_training(self, *args, **kwargs) -> bool:
@@ -390,10 +395,11 @@ class B200MultiRuntime(B200Runtime):
                 ak = np.ascontiguousarray(fam_approx, dtype=np.float64).reshape(-1)
                 if ak.size != K * n:
                     raise _lib.CbGpuError(_lib.ERR_INVALID, f"LengthMismatch: approx_k has {ak.size}, expected {K * n}")
-        t = None if target is None else np.ascontiguousarray(target, dtype=np.float64)
+        t = None if target is None else np.ascontiguousarray(target, dtype=np.float64).reshape(-1)
         s = None if sample is None or len(sample) == 0 else np.ascontiguousarray(sample, dtype=np.float64)
-        if t is not None and t.size != n:
-            raise _lib.CbGpuError(_lib.ERR_INVALID, f"LengthMismatch: target has {t.size}, expected {n}")
+        want = K * n if self.label_matrix else n
+        if t is not None and t.size != want:
+            raise _lib.CbGpuError(_lib.ERR_INVALID, f"LengthMismatch: target has {t.size}, expected {want}")
         sf = np.empty(D, dtype=np.int32)
         sb = np.empty(D, dtype=np.int32)
         ns = np.zeros(1, dtype=np.int32)

@@ -44,15 +44,17 @@ typedef enum {
     CBGPU_ERR_NO_DEVICE = 7   /* no CUDA device / library built without one */
 } cbgpu_status;
 
-/* Loss (runtime.rs:57-70): only the device-covered subset.  MultiClass is
- * served by the multi-output session (cbgpu_multi_begin_raw), QueryRMSE and
- * PairLogit by its ranking mode (cbgpu_rank_begin_raw); the scalar session
- * declines them. */
+/* Loss (runtime.rs:57-70, 186-260): only the device-covered subset.  The
+ * multi-output losses (MultiClass, MultiClassOneVsAll, MultiLogloss,
+ * MultiCrossEntropy) are served by the multi-output session
+ * (cbgpu_multi_begin_raw), the grouped losses by its ranking mode
+ * (cbgpu_rank_begin_raw); the scalar session declines them. */
 typedef enum {
     CBGPU_LOSS_RMSE = 0, CBGPU_LOSS_LOGLOSS = 1, CBGPU_LOSS_CROSSENTROPY = 2, CBGPU_LOSS_MULTICLASS = 3,
     CBGPU_LOSS_QUERYRMSE = 4, CBGPU_LOSS_PAIRLOGIT = 5, CBGPU_LOSS_PAIRLOGIT_PAIRWISE = 6,
     CBGPU_LOSS_QUERYSOFTMAX = 7, CBGPU_LOSS_LAMBDAMART = 8, CBGPU_LOSS_YETIRANK = 9,
-    CBGPU_LOSS_STOCHASTICRANK = 10, CBGPU_LOSS_YETIRANK_PAIRWISE = 11
+    CBGPU_LOSS_STOCHASTICRANK = 10, CBGPU_LOSS_YETIRANK_PAIRWISE = 11,
+    CBGPU_LOSS_MULTICLASS_ONE_VS_ALL = 12, CBGPU_LOSS_MULTILOGLOSS = 13, CBGPU_LOSS_MULTICROSSENTROPY = 14
 } cbgpu_loss;
 
 /* EScoreFunction (runtime.rs:834-864); Cosine is the default. */
@@ -258,11 +260,19 @@ CBGPU_API int cbgpu_histogram_noalloc(const uint8_t* d_bins_row_major, int64_t n
  * (crates/cb-train/src/boosting.rs:7400-8930 at approx_dimension K); this arm
  * reproduces that CPU branch on one GPU.
  *
- * cbgpu_multi_begin_raw: begin_device_training_raw's arguments (loss must be
- * CBGPU_LOSS_MULTICLASS; world_size 1) plus approx_dim = K (2..16).  Declines
- * (CBGPU_DECLINED) outside SymmetricTree / Plain / one fold / Cosine-L2 /
- * bootstrap No-Bayesian-Bernoulli / depth <= 10 / <= 255 borders.  The
- * approximant starts at 0 (MultiClass has no boost_from_average). */
+ * The diagonal losses MultiClassOneVsAll, MultiLogloss and MultiCrossEntropy
+ * (loss.rs:501-560) share the arm: per dimension p = sigmoid(a_d),
+ * der1 = t_d - p, der2 = -p (1 - p), and each dimension's Newton leaf is
+ * solved on its own (boosting.rs:8323-8420) instead of the coupled softmax
+ * solve.
+ *
+ * cbgpu_multi_begin_raw: begin_device_training_raw's arguments (loss one of
+ * CBGPU_LOSS_MULTICLASS, _MULTICLASS_ONE_VS_ALL, _MULTILOGLOSS,
+ * _MULTICROSSENTROPY; world_size 1) plus approx_dim = K (2..16; 1..16 for the
+ * two label losses).  Declines (CBGPU_DECLINED) outside SymmetricTree / Plain /
+ * one fold / Cosine-L2-Solar-LOO-Sat / bootstrap No-Bayesian-Bernoulli /
+ * depth <= 10 / <= 255 borders.  The approximant starts at 0 (no
+ * boost_from_average on this family). */
 typedef struct cbgpu_multi_session cbgpu_multi_session;
 CBGPU_API int cbgpu_multi_begin_raw(const cbgpu_begin_args* args, int32_t approx_dim,
                                     const float* const* float_columns, const double* borders_flat,
@@ -284,8 +294,11 @@ CBGPU_API int cbgpu_multi_begin_cat_raw(const cbgpu_begin_args* args, int32_t ap
 /* grow_tree_on_device with FamilyTreeArgs::MultiOutput (runtime.rs:1629):
  *  approx_k  [K * n] DIM-major approximant (approx_k[d * n + i]) or NULL for
  *            the resident approximant (advanced by learning_rate * leaf);
- *  target    [n] class index per object as a double (0..K-1), read on the
- *            first call;
+ *  target    read on the first call: [n] class index per object as a double
+ *            (0..K-1) for MultiClass and MultiClassOneVsAll; for MultiLogloss
+ *            ({0, 1}) and MultiCrossEntropy ([0, 1]) the [K * n] DIM-major
+ *            label matrix target[d * n + i], the reference's multilabel
+ *            layout;
  *  sample    the host bootstrap multiplier, as for cbgpu_grow_tree;
  *  leaf_values [2^depth * K] LEAF-major raw deltas (DeviceGrownTree's
  *            leaf_count x approx_dim block, runtime.rs:1008-1024), not scaled
