@@ -755,8 +755,22 @@ int orc_train(const orc_train_args* a, orc_train_out* o) {
     double prev_mean = 0.0;
     int rc = 0;
 
+    const int quantile = a->loss == ORC_LOSS_MAE || a->loss == ORC_LOSS_QUANTILE;
+    /* MAE is Quantile{alpha 0.5, delta 1e-6} (loss.rs:186-193) */
+    const double q_alpha = a->loss == ORC_LOSS_MAE ? 0.5 : a->quantile_alpha;
+    const double q_delta = a->loss == ORC_LOSS_MAE ? 1e-6 : a->quantile_delta;
+    float* res = a->exact_leaf ? (float*)malloc(sizeof(float) * (size_t)(n ? n : 1)) : NULL;
+    double* rw = a->exact_leaf ? (double*)malloc(sizeof(double) * (size_t)(n ? n : 1)) : NULL;
+
     for (int32_t it = 0; it < a->iterations; ++it) {
-        orc_compute_gradients(a->loss, approx, a->target, n, der1, NULL);
+        if (quantile) {
+            for (int64_t i = 0; i < n; ++i) { /* quantile_der1 (loss.rs:166-175) */
+                const double v = a->target[i] - approx[i];
+                der1[i] = fabs(v) < q_delta ? 0.0 : (v > 0.0 ? q_alpha : -(1.0 - q_alpha));
+            }
+        } else {
+            orc_compute_gradients(a->loss, approx, a->target, n, der1, NULL);
+        }
         for (int64_t i = 0; i < n; ++i) wd1[i] = der1[i] * w[i];
         if (draws) {
             (void)orc_rng_gen(&rng); /* PRE_TREE_DRAWS = 2 */
@@ -801,8 +815,22 @@ int orc_train(const orc_train_args* a, orc_train_out* o) {
         }
         double* lv = o->leaf_values + (size_t)it * L;
         for (int32_t k = 0; k < L; ++k) lv[k] = 0.0;
-        for (int32_t k = 0; k < nl; ++k)
-            lv[k] = calc_average(ls[2 * k], ls[2 * k + 1], scaled_l2) * lr;
+        if (a->exact_leaf) {
+            /* Exact: the leaf's members in object order, residual (f32)(t - a)
+             * and object weight (collect_leaf_residuals), no l2 */
+            for (int32_t k = 0; k < nl; ++k) {
+                int64_t m = 0;
+                for (int64_t i = 0; i < n; ++i)
+                    if (leaf[i] == k) {
+                        res[m] = (float)(a->target[i] - approx[i]);
+                        rw[m++] = w[i];
+                    }
+                lv[k] = orc_exact_leaf_delta(res, rw, m, q_alpha, q_delta) * lr;
+            }
+        } else {
+            for (int32_t k = 0; k < nl; ++k)
+                lv[k] = calc_average(ls[2 * k], ls[2 * k + 1], scaled_l2) * lr;
+        }
         for (int64_t i = 0; i < n; ++i) approx[i] += lv[leaf[i]];
         if (o->staged) memcpy(o->staged + (size_t)it * n, approx, sizeof(double) * (size_t)n);
         if (draws) {
@@ -818,8 +846,63 @@ int orc_train(const orc_train_args* a, orc_train_out* o) {
     }
     if (o->final_approx) memcpy(o->final_approx, approx, sizeof(double) * (size_t)n);
     free(w); free(approx); free(der1); free(wd1); free(dobj); free(sw); free(ctl);
-    free(sg); free(sh); free(leaf); free(ls);
+    free(sg); free(sh); free(leaf); free(ls); free(res); free(rw);
     return rc;
+}
+
+typedef struct {
+    float v;
+    double w;
+    int64_t pos;
+} orc_vw;
+
+static int vw_cmp(const void* x, const void* y) {
+    const orc_vw* a = (const orc_vw*)x;
+    const orc_vw* b = (const orc_vw*)y;
+    /* ascending value, ties by original position: a stable sort */
+    if (a->v < b->v) return -1;
+    if (a->v > b->v) return 1;
+    return a->pos < b->pos ? -1 : (a->pos > b->pos ? 1 : 0);
+}
+
+double orc_exact_leaf_delta(const float* residuals, const double* weights, int64_t n, double alpha, double delta) {
+    if (n == 0) return 0.0;
+    if (alpha <= 0.0) { /* the minimum element */
+        double mn = INFINITY;
+        for (int64_t i = 0; i < n; ++i)
+            if ((double)residuals[i] < mn) mn = (double)residuals[i];
+        return mn;
+    }
+    orc_vw* e = (orc_vw*)malloc(sizeof(orc_vw) * (size_t)n);
+    for (int64_t i = 0; i < n; ++i) {
+        e[i].v = residuals[i];
+        e[i].w = weights ? weights[i] : 1.0;
+        e[i].pos = i;
+    }
+    qsort(e, (size_t)n, sizeof(orc_vw), vw_cmp);
+    double total = 0.0;
+    for (int64_t i = 0; i < n; ++i) total += e[i].w; /* sum_f64 in sorted order */
+    const double need = total * alpha;
+    double acc = 0.0;
+    double q = (double)e[n - 1].v;
+    for (int64_t i = 0; i < n; ++i) {
+        acc += e[i].w;
+        if (acc >= need - DBL_EPSILON) {
+            q = (double)e[i].v;
+            break;
+        }
+    }
+    if (delta > 0.0) {
+        const float qf = (float)q;
+        double less = 0.0, equal = 0.0;
+        for (int64_t i = 0; i < n; ++i) {
+            if (e[i].v < qf) less += e[i].w;
+            else if (e[i].v == qf) equal += e[i].w;
+        }
+        q = less + equal * alpha >= need - DBL_EPSILON ? q - delta : q + delta;
+    }
+    free(e);
+    return q;
 }
 
 

@@ -90,7 +90,11 @@ void orc_apply_oblivious(const float* x_fm, int64_t n, int32_t F, const uint32_t
                          const uint8_t* nan_above, double* out);
 
 /* ---- derivatives (crates/cb-compute/src/loss.rs:35-80) ----------------- */
-enum { ORC_LOSS_RMSE = 0, ORC_LOSS_LOGLOSS = 1, ORC_LOSS_CROSSENTROPY = 2 };
+enum { ORC_LOSS_RMSE = 0, ORC_LOSS_LOGLOSS = 1, ORC_LOSS_CROSSENTROPY = 2, ORC_LOSS_MAE = 3, ORC_LOSS_QUANTILE = 4 };
+
+/* exact_leaf_delta (crates/cb-compute/src/leaf.rs:445-520): the weighted
+ * alpha-quantile of one leaf's f32 residuals with the delta adjustment. */
+double orc_exact_leaf_delta(const float* residuals, const double* weights, int64_t n, double alpha, double delta);
 void orc_compute_gradients(int32_t loss, const double* approx, const double* target, int64_t n,
                            double* der1, double* der2);
 
@@ -138,6 +142,11 @@ typedef struct {
      * (first-seen order) [n_cat][n]; split candidates are bin == value */
     int32_t n_cat;
     const uint8_t* cat_bins_fm;
+    /* MAE / Quantile: der1 = quantile_der1 (loss.rs:166-175); exact_leaf 1 takes
+     * the Exact leaf method (boosting.rs:2561-2606) instead of Gradient */
+    int32_t exact_leaf;
+    double quantile_alpha;
+    double quantile_delta;
 } orc_train_args;
 
 /* CalcCatFeatureHash (crates/cb-data/src/cat_hash.rs): CityHash64 (v1.0) of the

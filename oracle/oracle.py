@@ -17,7 +17,7 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 _LIB_PATH = os.path.join(_HERE, "liboracle.so")
 _lib = None
 
-LOSS = {"RMSE": 0, "Logloss": 1, "CrossEntropy": 2}
+LOSS = {"RMSE": 0, "Logloss": 1, "CrossEntropy": 2, "MAE": 3, "Quantile": 4}
 BOOT = {"No": 0, "Bayesian": 1, "Bernoulli": 2, "MVS": 3}
 SCORE = {"Cosine": 0, "L2": 1, "SolarL2": 2, "LOOL2": 5, "SatL2": 6}
 BORDER_TYPE = {"Median": 0, "GreedyLogSum": 1, "UniformAndQuantiles": 2, "MinEntropy": 3,
@@ -48,6 +48,7 @@ class _TrainArgs(C.Structure):
         ("random_strength", C.c_double), ("random_seed", C.c_uint64),
         ("boost_from_average", C.c_int32), ("n_threads", C.c_int32),
         ("n_cat", C.c_int32), ("cat_bins_fm", C.c_void_p),
+        ("exact_leaf", C.c_int32), ("quantile_alpha", C.c_double), ("quantile_delta", C.c_double),
     ]
 
 
@@ -154,6 +155,8 @@ def lib():
         L.orc_yeti_query_seeds.restype = None
         L.orc_yeti_recalc_seeds.argtypes = [C.c_uint64, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_void_p]
         L.orc_yeti_recalc_seeds.restype = None
+        L.orc_exact_leaf_delta.argtypes = [C.c_void_p, C.c_void_p, C.c_int64, C.c_double, C.c_double]
+        L.orc_exact_leaf_delta.restype = C.c_double
         L.orc_train.argtypes = [P(_TrainArgs), P(_TrainOut)]
         L.orc_train.restype = C.c_int
         _lib = L
@@ -335,10 +338,18 @@ class OracleFit:
 def train(bins_fm, border_counts, target, *, loss="RMSE", depth=6, iterations=10,
           learning_rate=0.1, l2_leaf_reg=3.0, score_function="Cosine", bootstrap_type="No",
           subsample=0.66, bagging_temperature=1.0, random_strength=0.0, random_seed=0,
-          boost_from_average=True, weights=None, staged=True, n_threads=0, cat_bins_fm=None) -> OracleFit:
+          boost_from_average=True, weights=None, staged=True, n_threads=0, cat_bins_fm=None,
+          leaf_estimation_method="Gradient", quantile_alpha=0.5, quantile_delta=1e-6) -> OracleFit:
     """The reference CPU boosting loop (crates/cb-train/src/boosting.rs) on quantized bins;
     cat_bins_fm [C, n] adds one-hot categorical features (split_feature >= F: cat feature
-    split_feature - F, passing on bin == split_bin)."""
+    split_feature - F, passing on bin == split_bin).  leaf_estimation_method "Exact" takes
+    each leaf's weighted quantile of the residuals (MAE / Quantile only, boosting.rs:2561-2606);
+    quantile_alpha / quantile_delta are Quantile's parameters (MAE is alpha 0.5, delta 1e-6)."""
+    if leaf_estimation_method not in ("Gradient", "Exact"):
+        raise ValueError(f"leaf method {leaf_estimation_method} is not restated")
+    exact = leaf_estimation_method == "Exact"
+    if exact and loss not in ("MAE", "Quantile"):
+        raise ValueError("the Exact leaf is restated for MAE and Quantile")
     bins = np.ascontiguousarray(bins_fm, dtype=np.uint8)
     F, n = bins.shape
     cb = None if cat_bins_fm is None else np.ascontiguousarray(cat_bins_fm, dtype=np.uint8).reshape(-1, n)
@@ -357,7 +368,8 @@ def train(bins_fm, border_counts, target, *, loss="RMSE", depth=6, iterations=10
     args = _TrainArgs(n, F, _p(bins), _p(bc), _p(t), _p(w), LOSS[loss], depth, iterations,
                       learning_rate, l2_leaf_reg, SCORE[score_function], BOOT[bootstrap_type],
                       subsample, bagging_temperature, random_strength, random_seed,
-                      1 if boost_from_average else 0, n_threads, 0 if cb is None else cb.shape[0], _p(cb))
+                      1 if boost_from_average else 0, n_threads, 0 if cb is None else cb.shape[0], _p(cb),
+                      1 if exact else 0, quantile_alpha, quantile_delta)
     out = _TrainOut(_p(sf), _p(sb), _p(td), _p(lv), _p(st), _p(fa), _p(bias), _p(calls))
     rc = lib().orc_train(C.byref(args), C.byref(out))
     if rc != 0:
@@ -421,6 +433,12 @@ def train_multiclass(bins_fm, border_counts, target_class, n_classes, *, depth=6
     if rc != 0:
         raise RuntimeError(f"orc_train_multiclass failed rc={rc}")
     return OracleMultiFit(sf, sb, td, lv, st, fa)
+
+
+def exact_leaf_delta(residuals, weights, alpha=0.5, delta=1e-6) -> float:
+    r = np.ascontiguousarray(residuals, dtype=np.float32)
+    w = None if weights is None else np.ascontiguousarray(weights, dtype=np.float64)
+    return lib().orc_exact_leaf_delta(_p(r), _p(w), r.size, alpha, delta)
 
 
 def solve_symmetric_newton(sum_der, sum_der2_packed, scaled_l2):

@@ -158,6 +158,22 @@ def e2e_fixtures(ref):
         _save(scen, Xs, ld(scen, "y.npy"), [list(r) for r in B], _params(cfg["params"], "RMSE"), model,
               weights=w, extra={"predictions": preds})
         written.append(scen)
+    # Exact leaves: Quantile / MAE on numeric_tiny (model borders) and the
+    # device-parity pair with their full frozen border sets
+    for scen, alpha in (("quantile_alpha05_mae", 0.5), ("quantile_alpha07", 0.7)):
+        cfg, model = jl(scen, "config.json"), jl(scen, "model.json")
+        p = dict(_params(cfg["params"], "Quantile"), leaf_estimation_method="Exact", quantile_alpha=alpha,
+                 quantile_delta=1e-6)
+        _save(scen, Xt, yt, borders_of(model), p, model, ld(scen, "staged.npy"))
+        written.append(scen)
+    for sub, loss, alpha in (("mae", "MAE", 0.5), ("quantile07", "Quantile", 0.7)):
+        scen = f"exact_leaf_device/{sub}"
+        cfg, model = jl(scen, "config.json"), jl(scen, "model.json")
+        p = dict(_params(cfg["params"], loss), leaf_estimation_method="Exact", quantile_alpha=alpha,
+                 quantile_delta=1e-6)
+        _save(f"exact_leaf_{sub}", ld(scen, "X.npy"), ld(scen, "y.npy"), [list(r) for r in ld(scen, "borders.npy")],
+              p, model, extra={"predictions": ld(scen, "predictions.npy")})
+        written.append(scen)
     # NaN handling, both sentinel modes (model borders carry the sentinel)
     cfg = jl("nan_mode", "config.json")
     for mode in ("Min", "Max"):

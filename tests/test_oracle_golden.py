@@ -88,7 +88,8 @@ def _oracle_fit(sc, staged=True):
         subsample=p["subsample"], bagging_temperature=p["bagging_temperature"],
         random_strength=p["random_strength"], random_seed=p["random_seed"],
         boost_from_average=p["boost_from_average"], weights=sc.get("weights"), staged=staged,
-        n_threads=1)
+        n_threads=1, leaf_estimation_method=p.get("leaf_estimation_method", "Gradient"),
+        quantile_alpha=p.get("quantile_alpha", 0.5), quantile_delta=p.get("quantile_delta", 1e-6))
 
 
 def _first_tree_only(sc):
