@@ -34,7 +34,8 @@ class BeginArgs(C.Structure):
         ("bias", C.c_double), ("sample_from_host", C.c_int32), ("random_strength", C.c_double),
         ("device", C.c_int32), ("rank", C.c_int32), ("world_size", C.c_int32),
         ("row_offset", C.c_int64), ("n_total", C.c_int64), ("nccl_unique_id", C.c_void_p),
-        ("border_counts", C.c_void_p),
+        ("border_counts", C.c_void_p), ("exact_leaf", C.c_int32), ("quantile_alpha", C.c_double),
+        ("quantile_delta", C.c_double),
     ]
 
 

@@ -42,6 +42,9 @@ class FitParams:
     srank_sigma: float = 1.0
     srank_mu: float = 0.0
     srank_num_estimations: int = 1
+    leaf_estimation_method: str = "Gradient"  # "Exact" for MAE / Quantile
+    quantile_alpha: float = 0.5    # Quantile:alpha
+    quantile_delta: float = 1e-6   # Quantile:delta
 
 
 @dataclass
@@ -123,7 +126,9 @@ def fit(float_columns: Sequence[np.ndarray], borders: Sequence[Sequence[float]],
                             bagging_temperature=p.bagging_temperature, device=device,
                             rank=pl.get("rank", 0), world_size=pl.get("world_size", 1),
                             row_offset=pl.get("row_offset", 0), n_total=n_total,
-                            nccl_unique_id=pl.get("nccl_unique_id"))
+                            nccl_unique_id=pl.get("nccl_unique_id"),
+                            exact_leaf=p.leaf_estimation_method == "Exact", quantile_alpha=p.quantile_alpha,
+                            quantile_delta=p.quantile_delta)
     rt = B200Runtime()
     ok = rt.begin_device_training_raw(p.loss, p.depth, True, 1, p.score_function, cols, borders, w,
                                       n, F, n_bins, lr, scaled_l2, cfg)

@@ -15,6 +15,10 @@
 
 #include "kernels.cuh"
 
+#include <cub/block/block_reduce.cuh>
+#include <cub/block/block_scan.cuh>
+#include <cub/device/device_radix_sort.cuh>
+
 namespace cbgpu {
 
 namespace {
@@ -421,8 +425,14 @@ __device__ __forceinline__ double sample_of(int s_mode, const float* sw32, const
 // approx += lr * leaf value of the previous tree (when pending), then
 // der1 (RMSE t - a; Logloss t - (1 - 1/(1 + e^a))), wd1 = der1 * w, and the
 // maxima of |g| = |wd1 * s|, |h| = |w * s|, |wd1|, |w| for the fixed-point scales.
-__device__ __forceinline__ double der1_of(int loss, double a, double t) {
+// MAE / Quantile (loss ids 15, 16): quantile_der1 (loss.rs:166-175), 0 inside
+// |t - a| < delta, else alpha above and -(1 - alpha) below.
+__device__ __forceinline__ double der1_of(int loss, double a, double t, double qa, double qd) {
     if (loss == 0) return __dsub_rn(t, a);
+    if (loss >= 15) {
+        const double v = __dsub_rn(t, a);
+        return fabs(v) < qd ? 0.0 : (v > 0.0 ? qa : -__dsub_rn(1.0, qa));
+    }
     const double e = exp(a);
     const double p = __dsub_rn(1.0, __ddiv_rn(1.0, __dadd_rn(1.0, e)));
     return __dsub_rn(t, p);
@@ -436,6 +446,7 @@ __global__ void __launch_bounds__(256) der_kernel(
     const double* __restrict__ lrv_in, const TreeParams* __restrict__ tp, int s_mode, const float* __restrict__ sw32,
     const double* __restrict__ sw64, double* __restrict__ wd1, TreeState* ts, bool defer) {
     const double* lrv = tp->pending ? lrv_in : nullptr;
+    const double qa = tp->q_alpha, qd = tp->q_delta;
     double m[4] = {0.0, 0.0, 0.0, 0.0};
     bool bad = false;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -458,7 +469,7 @@ __global__ void __launch_bounds__(256) der_kernel(
             const int64_t i = i0 + k * stride;
             if (i >= n) continue;
             if (lrv) approx[i] = a[k];
-            const double wd = __dmul_rn(der1_of(loss, a[k], t[k]), w[k]);
+            const double wd = __dmul_rn(der1_of(loss, a[k], t[k], qa, qd), w[k]);
             wd1[i] = wd;
             m[2] = fmax(m[2], fabs(wd));
             m[3] = fmax(m[3], fabs(w[k]));
@@ -1722,6 +1733,139 @@ void launch_gradients(int64_t n, int loss, const double* approx, const double* t
     if (blocks > 148 * 8) blocks = 148 * 8;
     if (blocks < 1) return;
     gradients_kernel<<<(unsigned)blocks, 256, 0, st>>>(n, loss, approx, target, d1, d2);
+}
+
+
+// ---- Exact leaves: MAE / Quantile (leaf.rs:445-520, boosting.rs:2561-2606) ----
+
+// f32 bit pattern -> an unsigned key in f32::total_cmp order
+__device__ __forceinline__ uint32_t f32_total_order(float v) {
+    const uint32_t b = __float_as_uint(v);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+__device__ __forceinline__ float f32_from_total_order(uint32_t u) {
+    return __uint_as_float((u & 0x80000000u) ? (u ^ 0x80000000u) : ~u);
+}
+
+// keys[i] = leaf << 32 | order(f32(t - a)) (the residuals the CPU collects
+// through f32, collect_leaf_residuals), w[i] = the object weight
+__global__ void exact_keys_kernel(int64_t n, const double* __restrict__ approx, const double* __restrict__ target,
+                                  const double* __restrict__ weight, const uint16_t* __restrict__ leaf,
+                                  ull* __restrict__ keys, double* __restrict__ w) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const float r = __double2float_rn(__dsub_rn(target[i], approx[i]));
+        keys[i] = ((ull)leaf[i] << 32) | f32_total_order(r);
+        w[i] = weight ? weight[i] : 1.0;
+    }
+}
+
+constexpr int kExactThreads = 512;
+
+// first index in [lo, hi) whose key's leaf part is >= q
+__device__ __forceinline__ int64_t exact_leaf_start(const ull* keys, int64_t lo, int64_t hi, ull q) {
+    while (lo < hi) {
+        const int64_t mid = lo + (hi - lo) / 2;
+        if ((keys[mid] >> 32) < q) lo = mid + 1;
+        else hi = mid;
+    }
+    return lo;
+}
+
+// One block per leaf over its sorted members: total weight, the first member
+// whose running weight reaches total * alpha - DBL_EPSILON (the last member if
+// none), then the delta adjustment from the weights below / equal to it.  The
+// block sums add in tree order, so they equal the CPU's sequential sums when
+// the partial sums are exact in f64 (unit, integer or dyadic weights) and
+// differ by rounding otherwise.
+__global__ void __launch_bounds__(kExactThreads)
+exact_leaf_kernel(int64_t n, const ull* __restrict__ keys, const double* __restrict__ w, double alpha,
+                  double delta, double lr, double* __restrict__ leaf_raw, double* __restrict__ leaf_lrv) {
+    using Reduce = cub::BlockReduce<double, kExactThreads>;
+    using Scan = cub::BlockScan<double, kExactThreads>;
+    __shared__ union {
+        typename Reduce::TempStorage r;
+        typename Scan::TempStorage s;
+    } tmp;
+    __shared__ int64_t s_lo, s_hi, s_hit;
+    __shared__ double s_val;
+    const ull q = blockIdx.x;
+    if (threadIdx.x == 0) {
+        s_lo = exact_leaf_start(keys, 0, n, q);
+        s_hi = exact_leaf_start(keys, s_lo, n, q + 1);
+        s_hit = INT64_MAX;
+    }
+    __syncthreads();
+    const int64_t lo = s_lo, hi = s_hi;
+    double out = 0.0;
+    if (hi > lo && alpha <= 0.0) {
+        out = (double)f32_from_total_order((uint32_t)keys[lo]);  // the minimum element
+    } else if (hi > lo) {
+        double part = 0.0;
+        for (int64_t i = lo + threadIdx.x; i < hi; i += kExactThreads) part = __dadd_rn(part, w[i]);
+        const double total = Reduce(tmp.r).Sum(part);
+        if (threadIdx.x == 0) s_val = total;
+        __syncthreads();
+        const double need = __dmul_rn(s_val, alpha);
+        const double bar = __dsub_rn(need, DBL_EPSILON);
+        double carry = 0.0;
+        for (int64_t base = lo; base < hi; base += kExactThreads) {
+            const int64_t i = base + threadIdx.x;
+            const double v = i < hi ? w[i] : 0.0;
+            double inc, chunk;
+            Scan(tmp.s).InclusiveSum(v, inc, chunk);
+            __syncthreads();
+            if (i < hi && __dadd_rn(carry, inc) >= bar) atomicMin((unsigned long long*)&s_hit, (unsigned long long)i);
+            __syncthreads();
+            if (s_hit != INT64_MAX) break;
+            carry = __dadd_rn(carry, chunk);
+        }
+        const int64_t j = s_hit != INT64_MAX ? s_hit : hi - 1;
+        const float qf = f32_from_total_order((uint32_t)keys[j]);
+        double qv = (double)qf;
+        if (delta > 0.0) {
+            double less = 0.0, equal = 0.0;
+            for (int64_t i = lo + threadIdx.x; i < hi; i += kExactThreads) {
+                const float v = f32_from_total_order((uint32_t)keys[i]);
+                if (v < qf) less = __dadd_rn(less, w[i]);
+                else if (v == qf) equal = __dadd_rn(equal, w[i]);
+            }
+            __syncthreads();
+            const double ls = Reduce(tmp.r).Sum(less);
+            __syncthreads();
+            const double es = Reduce(tmp.r).Sum(equal);
+            if (threadIdx.x == 0) s_val = __dadd_rn(ls, __dmul_rn(es, alpha)) >= bar ? 1.0 : 0.0;
+            __syncthreads();
+            qv = s_val != 0.0 ? __dsub_rn(qv, delta) : __dadd_rn(qv, delta);
+        }
+        out = qv;
+    }
+    if (threadIdx.x == 0) {
+        leaf_raw[q] = out;
+        leaf_lrv[q] = __dmul_rn(out, lr);
+    }
+}
+
+size_t exact_sort_scratch_bytes(int64_t n) {
+    size_t bytes = 0;
+    cub::DeviceRadixSort::SortPairs(nullptr, bytes, (const ull*)nullptr, (ull*)nullptr, (const double*)nullptr,
+                                    (double*)nullptr, (int)(n > 0 ? n : 1), 0, 48);
+    return bytes;
+}
+
+void launch_exact_leaves(int depth, int64_t n, const double* approx, const double* target, const double* weight,
+                         const uint16_t* leaf, ull* keys, ull* keys_sorted, double* w, double* w_sorted, void* tmp,
+                         size_t tmp_bytes, double alpha, double delta, double lr, double* leaf_raw,
+                         double* leaf_lrv, cudaStream_t st) {
+    int64_t blocks = (n + 255) / 256;
+    if (blocks > 148 * 8) blocks = 148 * 8;
+    if (blocks < 1) blocks = 1;
+    exact_keys_kernel<<<(unsigned)blocks, 256, 0, st>>>(n, approx, target, weight, leaf, keys, w);
+    size_t bytes = tmp_bytes;
+    cub::DeviceRadixSort::SortPairs(tmp, bytes, (const ull*)keys, keys_sorted, (const double*)w, w_sorted, (int)n, 0,
+                                    32 + depth, st);
+    exact_leaf_kernel<<<1u << depth, kExactThreads, 0, st>>>(n, keys_sorted, w_sorted, alpha, delta, lr, leaf_raw,
+                                                             leaf_lrv);
 }
 
 }  // namespace cbgpu

@@ -44,6 +44,8 @@ struct TreeParams {
     double mvs_lambda;
     int32_t pending;     // apply the previous tree's leaf values before the derivatives
     int32_t pad;
+    double q_alpha;      // MAE / Quantile: quantile_der1's alpha and delta
+    double q_delta;
 };
 
 struct TreeState {
@@ -150,6 +152,16 @@ void launch_small_side(int level_next, const uint32_t* child_cnt_global, uint8_t
 void launch_route_leafsum(int depth, int64_t n, const uint8_t* bins_fm, int64_t n_stride, uint16_t* leaf,
                           const double* wd1, const double* weight, TreeState* ts, ull* leaf_sums,
                           cudaStream_t st);
+// Exact leaves (MAE / Quantile): keys[i] = leaf << 32 | total-order bits of
+// the f32 residual, sorted with the weights, then one block per leaf takes
+// the weighted alpha-quantile into leaf_raw / leaf_lrv.  tmp / tmp_bytes is
+// the radix sort's scratch (exact_sort_scratch_bytes).
+size_t exact_sort_scratch_bytes(int64_t n);
+void launch_exact_leaves(int depth, int64_t n, const double* approx, const double* target, const double* weight,
+                         const uint16_t* leaf, ull* keys, ull* keys_sorted, double* w, double* w_sorted, void* tmp,
+                         size_t tmp_bytes, double alpha, double delta, double lr, double* leaf_raw,
+                         double* leaf_lrv, cudaStream_t st);
+
 void launch_leaf_values(int depth, int n_splits_expected, const ull* leaf_sums, double l2, double lr,
                         TreeState* ts, double* leaf_raw, double* leaf_lrv, cudaStream_t st);
 void launch_leaf_export(int64_t n, const uint16_t* leaf, void* out, int bytes, cudaStream_t st);

@@ -130,6 +130,13 @@ struct cbgpu_session {
     // configuration
     int device = 0;
     int loss = 0, depth = 0, score_fn = 0, boot = 0, sample_from_host = 0;
+    // Exact leaves (MAE / Quantile): quantile_der1's alpha / delta, sort buffers
+    int exact = 0;
+    double q_alpha = 0.5, q_delta = 1e-6;
+    ull *ex_keys = nullptr, *ex_keys_sorted = nullptr;
+    double *ex_w = nullptr, *ex_w_sorted = nullptr;
+    void* ex_tmp = nullptr;
+    size_t ex_tmp_bytes = 0;
     float sample_rate = 1.0f, temp = 1.0f;
     int has_mvs_lambda = 0;
     double mvs_lambda = 0.0;
@@ -227,7 +234,22 @@ int check_args(const cbgpu_begin_args* a) {
         return fail(CBGPU_DECLINED, "grow_policy %d is not SymmetricTree", a->grow_policy);
     if (!a->boosting_type_is_plain) return fail(CBGPU_DECLINED, "Ordered boosting is not covered");
     if (a->fold_count != 1) return fail(CBGPU_DECLINED, "fold_count %d != 1", a->fold_count);
-    if (a->loss < 0 || a->loss > 2) return fail(CBGPU_DECLINED, "loss %d not covered", a->loss);
+    const bool quantile = a->loss == CBGPU_LOSS_MAE || a->loss == CBGPU_LOSS_QUANTILE;
+    if ((a->loss < 0 || a->loss > 2) && !quantile) return fail(CBGPU_DECLINED, "loss %d not covered", a->loss);
+    // map_leaf_method (session.rs:1176-1200): MAE / Quantile only with Exact
+    // leaves, Exact only for them, and only without draws on one rank
+    if (quantile != (a->exact_leaf != 0))
+        return fail(CBGPU_DECLINED, a->exact_leaf ? "Exact leaves are covered for MAE / Quantile only"
+                                                  : "MAE / Quantile are covered with Exact leaves only");
+    if (a->exact_leaf) {
+        if (a->bootstrap_type != CBGPU_BOOT_NO || a->sample_from_host || a->has_mvs_lambda)
+            return fail(CBGPU_DECLINED, "Exact leaves need bootstrap No");
+        if (a->world_size != 1) return fail(CBGPU_DECLINED, "Exact leaves run on one rank");
+        if (a->n >= (int64_t)0x7fffffff) return fail(CBGPU_DECLINED, "Exact leaves: n >= 2^31 rows");
+        if (a->loss == CBGPU_LOSS_QUANTILE && !(a->quantile_alpha >= 0.0 && a->quantile_alpha <= 1.0 &&
+                                                 a->quantile_delta >= 0.0))
+            return fail(CBGPU_ERR_INVALID, "Quantile alpha %g / delta %g", a->quantile_alpha, a->quantile_delta);
+    }
     if (a->score_function != CBGPU_SCORE_COSINE && a->score_function != CBGPU_SCORE_L2 &&
         a->score_function != CBGPU_SCORE_SOLAR_L2 && a->score_function != CBGPU_SCORE_LOO_L2 &&
         a->score_function != CBGPU_SCORE_SAT_L2)
@@ -257,6 +279,11 @@ int alloc_session(cbgpu_session* s, const cbgpu_begin_args* a) {
     CU(cudaSetDevice(s->device));
     CU(cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking));
     s->loss = a->loss;
+    s->exact = a->exact_leaf ? 1 : 0;
+    if (a->loss == CBGPU_LOSS_QUANTILE) {  // MAE keeps the median anchor 0.5 / 1e-6 (loss.rs:186-193)
+        s->q_alpha = a->quantile_alpha;
+        s->q_delta = a->quantile_delta;
+    }
     s->depth = a->depth;
     s->score_fn = a->score_function;
     s->boot = a->bootstrap_type;
@@ -328,6 +355,14 @@ int alloc_session(cbgpu_session* s, const cbgpu_begin_args* a) {
     DA(s->leaf_sums, 2 * L);
     DA(s->leaf_raw, L);
     DA(s->leaf_lrv, L);
+    if (s->exact) {
+        DA(s->ex_keys, s->n);
+        DA(s->ex_keys_sorted, s->n);
+        DA(s->ex_w, s->n);
+        DA(s->ex_w_sorted, s->n);
+        s->ex_tmp_bytes = exact_sort_scratch_bytes(s->n);
+        DA(*(char**)&s->ex_tmp, s->ex_tmp_bytes);
+    }
     DA(s->ts, 1);
     DA(s->d_err, 1);
     DA(s->d_tp, 1);
@@ -377,7 +412,8 @@ void free_session(cbgpu_session* s) {
                     s->wd1, s->qstats, s->sw32, s->sw64, s->mvs_thr, s->leaf, s->perm[0], s->perm[1],
                     s->seg_mem, s->blk_true, s->child_cnt, s->flags, s->small_side, s->chunks, s->n_chunks, s->built,
                     s->hist[0], s->hist[1], s->feat_score, s->feat_bin, s->best_all, s->leaf_sums, s->leaf_raw,
-                    s->leaf_lrv, s->ts, s->d_err, s->leaf_export, s->d_tp};
+                    s->leaf_lrv, s->ts, s->d_err, s->leaf_export, s->d_tp, s->ex_keys, s->ex_keys_sorted,
+                    s->ex_w, s->ex_w_sorted, s->ex_tmp};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     void* hptrs[] = {s->h_ts, s->h_raw, s->h_tp};
@@ -619,6 +655,12 @@ int enqueue_tree(cbgpu_session* s, int set, bool prof, int boot_mode, int s_mode
     }
     launch_leaf_values(D, D, s->leaf_sums, s->l2, s->lr, s->ts, s->leaf_raw, s->leaf_lrv, st);
     ++launches;
+    if (s->exact) {  // the Exact leaf values replace the Gradient ones (boosting.rs:2561-2606)
+        launch_exact_leaves(D, s->n, s->approx, s->target, s->weight, s->leaf, s->ex_keys, s->ex_keys_sorted,
+                            s->ex_w, s->ex_w_sorted, s->ex_tmp, s->ex_tmp_bytes, s->q_alpha, s->q_delta, s->lr,
+                            s->leaf_raw, s->leaf_lrv, st);
+        launches += 2;
+    }
     CU(cudaGetLastError());
     CU(cudaMemcpyAsync(s->h_ts, s->ts, sizeof(TreeState), cudaMemcpyDeviceToHost, st));
     CU(cudaMemcpyAsync(s->h_raw, s->leaf_raw, sizeof(double) * L, cudaMemcpyDeviceToHost, st));
@@ -740,6 +782,8 @@ int grow(cbgpu_session* s, const double* approx_h, const double* target_h, int64
         }
     }
     tp.pending = s->pending ? 1 : 0;
+    tp.q_alpha = s->q_alpha;
+    tp.q_delta = s->q_delta;
     CU(cudaMemcpyAsync(s->d_tp, s->h_tp, sizeof(TreeParams), cudaMemcpyHostToDevice, st));
     s->pending = false;
 

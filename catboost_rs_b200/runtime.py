@@ -21,7 +21,7 @@ from . import _lib
 LOSS = {"RMSE": 0, "Rmse": 0, "Logloss": 1, "CrossEntropy": 2, "MultiClass": 3, "QueryRMSE": 4, "PairLogit": 5,
         "PairLogitPairwise": 6, "QuerySoftMax": 7,
         "LambdaMart": 8, "YetiRank": 9, "StochasticRank": 10, "YetiRankPairwise": 11, "MultiClassOneVsAll": 12,
-        "MultiLogloss": 13, "MultiCrossEntropy": 14}
+        "MultiLogloss": 13, "MultiCrossEntropy": 14, "MAE": 15, "Quantile": 16}
 # multi-output losses whose target is the [K, n] label matrix (dim-major)
 LABEL_MATRIX_LOSSES = ("MultiLogloss", "MultiCrossEntropy")
 LAMBDAMART_METRIC = {"NDCG": 0, "DCG": 1, "MRR": 2, "ERR": 3, "MAP": 4}
@@ -46,6 +46,10 @@ class DeviceTrainConfig:
     bagging_temperature: float = 1.0
     random_strength: float = 0.0
     border_counts: Optional[Sequence[int]] = None
+    # Exact leaves for MAE / Quantile (DeviceTrainConfig::exact_leaf, quantile_alpha / _delta)
+    exact_leaf: bool = False
+    quantile_alpha: float = 0.5
+    quantile_delta: float = 1e-6
     # document sharding (one process per GPU)
     device: int = 0
     rank: int = 0
@@ -152,6 +156,9 @@ class B200Runtime:
         a.n_total = cfg.n_total if cfg.n_total is not None else n
         a.nccl_unique_id = _ptr(uid)
         a.border_counts = _ptr(bc)
+        a.exact_leaf = 1 if cfg.exact_leaf else 0
+        a.quantile_alpha = cfg.quantile_alpha
+        a.quantile_delta = cfg.quantile_delta
         return a
 
     def _finish_begin(self, rc, n, depth) -> bool:

@@ -54,7 +54,8 @@ typedef enum {
     CBGPU_LOSS_QUERYRMSE = 4, CBGPU_LOSS_PAIRLOGIT = 5, CBGPU_LOSS_PAIRLOGIT_PAIRWISE = 6,
     CBGPU_LOSS_QUERYSOFTMAX = 7, CBGPU_LOSS_LAMBDAMART = 8, CBGPU_LOSS_YETIRANK = 9,
     CBGPU_LOSS_STOCHASTICRANK = 10, CBGPU_LOSS_YETIRANK_PAIRWISE = 11,
-    CBGPU_LOSS_MULTICLASS_ONE_VS_ALL = 12, CBGPU_LOSS_MULTILOGLOSS = 13, CBGPU_LOSS_MULTICROSSENTROPY = 14
+    CBGPU_LOSS_MULTICLASS_ONE_VS_ALL = 12, CBGPU_LOSS_MULTILOGLOSS = 13, CBGPU_LOSS_MULTICROSSENTROPY = 14,
+    CBGPU_LOSS_MAE = 15, CBGPU_LOSS_QUANTILE = 16  /* the scalar session, Exact leaves only */
 } cbgpu_loss;
 
 /* EScoreFunction (runtime.rs:834-864); Cosine is the default. */
@@ -111,6 +112,16 @@ typedef struct {
      * feature, as the reference device scorer does (kernels.rs:4687-4712).
      * cbgpu_begin_raw takes the counts from its border lists. */
     const int32_t* border_counts;
+    /* DeviceTrainConfig::exact_leaf / quantile_alpha / quantile_delta
+     * (session.rs:1176-1200): 1 takes each leaf's weighted alpha-quantile of
+     * the f32 residuals t - a (leaf.rs:445-520) for CBGPU_LOSS_MAE (alpha 0.5,
+     * delta 1e-6) or CBGPU_LOSS_QUANTILE (these alpha / delta); the structure
+     * comes from quantile_der1 (loss.rs:166-175).  Needs bootstrap No and one
+     * rank; 0 with MAE / Quantile, or 1 with another loss, declines.  A zeroed
+     * tail (callers built before these fields) means 0. */
+    int32_t exact_leaf;
+    double quantile_alpha;
+    double quantile_delta;
 } cbgpu_begin_args;
 
 typedef struct cbgpu_session cbgpu_session;

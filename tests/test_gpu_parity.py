@@ -140,7 +140,9 @@ def test_device_fit_matches_upstream_fixture(name):
                       learning_rate=p["learning_rate"], l2_leaf_reg=p["l2_leaf_reg"],
                       score_function=p["score_function"], bootstrap_type=p["bootstrap_type"],
                       subsample=p["subsample"], bagging_temperature=p["bagging_temperature"],
-                      random_seed=p["random_seed"], boost_from_average=p["boost_from_average"])
+                      random_seed=p["random_seed"], boost_from_average=p["boost_from_average"],
+                      leaf_estimation_method=p.get("leaf_estimation_method", "Gradient"),
+                      quantile_alpha=p.get("quantile_alpha", 0.5), quantile_delta=p.get("quantile_delta", 1e-6))
     X = sc["X"]
     m = cb.fit(_cols(X), sc["borders"], sc["y"], fp, weights=sc.get("weights"), staged=True)
     np.testing.assert_array_equal(m.split_feature, sc["split_feature"])
