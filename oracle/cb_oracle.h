@@ -191,8 +191,9 @@ typedef struct {
     int32_t n_cat;                 /* one-hot cat features (plain search only) */
     const uint8_t* cat_bins_fm;    /* [n_cat][n] first-seen perfect-hash bins */
     int32_t loss_kind;             /* 0: MultiClass softmax; 1: diagonal logistic
-                                      (MultiClassOneVsAll / MultiLogloss / MultiCrossEntropy) */
-    const double* target_matrix;   /* [K][n] per-dimension targets for loss_kind 1 */
+                                      (MultiClassOneVsAll / MultiLogloss / MultiCrossEntropy);
+                                      2: RMSEWithUncertainty (K = 2, [mean, log-scale]) */
+    const double* target_matrix;   /* [K][n] per-dimension targets for loss_kind 1; [n] for 2 */
 } orc_multi_args;
 
 typedef struct {

@@ -400,9 +400,23 @@ int orc_train_multiclass(const orc_multi_args* a, orc_multi_out* o) {
 
     size_t nk = (size_t)n * K;
     double* approx = (double*)calloc(nk + 1, sizeof(double)); /* [K][n], bias 0 */
+    if (a->loss_kind == 2 && n > 0) {
+        /* RMSEWithUncertainty starts at [mean, 0.5 ln var] (boosting.rs:1895-1914,
+         * 5190-5208): the f32 mean, the population variance about it in f32 */
+        const double mean = (double)(float)(orc_sum_f64(a->target_matrix, n) / (double)n);
+        double* sq = (double*)malloc(sizeof(double) * (size_t)n);
+        for (int64_t i = 0; i < n; ++i) sq[i] = (a->target_matrix[i] - mean) * (a->target_matrix[i] - mean);
+        const float var = (float)(orc_sum_f64(sq, n) / (double)n);
+        free(sq);
+        const double log_scale = 0.5 * log((double)var);
+        for (int64_t i = 0; i < n; ++i) {
+            approx[i] = mean;
+            approx[(size_t)n + i] = log_scale;
+        }
+    }
     double* wd1 = (double*)malloc(sizeof(double) * (nk + 1));  /* [K][n] */
     double* d2p = (double*)malloc(sizeof(double) * ((size_t)n * pk + 1));
-    const int diag = a->loss_kind == 1;
+    const int diag = a->loss_kind == 1 || a->loss_kind == 2;
     double* sg = (double*)malloc(sizeof(double) * (nk + 1));
     double* sh = (double*)malloc(sizeof(double) * ((size_t)n + 1));
     double* dobj = (double*)malloc(sizeof(double) * ((size_t)n + 1));
@@ -422,6 +436,21 @@ int orc_train_multiclass(const orc_multi_args* a, orc_multi_out* o) {
     int rc = 0;
     for (int32_t it = 0; it < a->iterations; ++it) {
         for (int64_t i = 0; i < n; ++i) {
+            if (a->loss_kind == 2) {
+                /* rmse_with_uncertainty_ders (loss.rs:680-720): diff = t - a0,
+                 * prec = exp(-2 a1); der1 = [diff, diff^2 prec - 1],
+                 * der2 = [-1, -2 diff^2 prec], the weight folded in once below */
+                const double t = a->target_matrix[i];
+                const double diff = t - approx[i];
+                const double prec = exp(-2.0 * approx[(size_t)n + i]);
+                const double dsp = diff * diff * prec;
+                wd1[i] = w[i] * diff;
+                wd1[(size_t)n + i] = w[i] * (dsp - 1.0);
+                d2p[(size_t)i * pk] = -1.0;
+                d2p[(size_t)i * pk + 1] = -2.0 * dsp;
+                for (int32_t j = 2; j < pk; ++j) d2p[(size_t)i * pk + j] = 0.0;
+                continue;
+            }
             if (diag) {
                 /* multiclass_onevsall_ders / multi_crossentropy_ders (loss.rs:501-560):
                  * per dimension p = sigmoid(a_d), der1 = t_d - p, der2 = -p (1 - p) */

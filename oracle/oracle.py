@@ -387,7 +387,7 @@ class OracleMultiFit:
     final_approx: np.ndarray   # [n, K]
 
 
-MULTI_LOSSES = ("MultiClass", "MultiClassOneVsAll", "MultiLogloss", "MultiCrossEntropy")
+MULTI_LOSSES = ("MultiClass", "MultiClassOneVsAll", "MultiLogloss", "MultiCrossEntropy", "RMSEWithUncertainty")
 
 
 def train_multiclass(bins_fm, border_counts, target_class, n_classes, *, depth=6, iterations=10,
@@ -414,6 +414,11 @@ def train_multiclass(bins_fm, border_counts, target_class, n_classes, *, depth=6
     elif loss == "MultiClassOneVsAll":
         y = np.ascontiguousarray(target_class, dtype=np.int32)
         tm = np.ascontiguousarray((np.arange(K)[:, None] == y[None, :]).astype(np.float64))
+    elif loss == "RMSEWithUncertainty":
+        if K != 2:
+            raise ValueError("RMSEWithUncertainty has two dimensions")
+        tm = np.ascontiguousarray(target_class, dtype=np.float64).reshape(n)
+        y = None
     else:
         tm = np.ascontiguousarray(target_class, dtype=np.float64).reshape(K, n)
         y = None
@@ -427,7 +432,7 @@ def train_multiclass(bins_fm, border_counts, target_class, n_classes, *, depth=6
     fa = np.empty((n, K), dtype=np.float64)
     args = _MultiArgs(n, F, _p(bins), _p(bc), _p(y), _p(w), K, depth, iterations, learning_rate, l2_leaf_reg,
                       SCORE[score_function], BOOT[bootstrap_type], subsample, bagging_temperature, random_seed,
-                      n_threads, 0 if cb is None else cb.shape[0], _p(cb), 0 if tm is None else 1, _p(tm))
+                      n_threads, 0 if cb is None else cb.shape[0], _p(cb), 0 if tm is None else (2 if loss == "RMSEWithUncertainty" else 1), _p(tm))
     out = _MultiOut(_p(sf), _p(sb), _p(td), _p(lv), _p(st), _p(fa))
     rc = lib().orc_train_multiclass(C.byref(args), C.byref(out))
     if rc != 0:

@@ -250,8 +250,8 @@ def multiclass_fixture(ref):
 
 
 def multi_output_fixtures(ref):
-    """Upstream MultiClassOneVsAll, MultiLogloss and MultiCrossEntropy fixtures
-    on numeric_tiny (Newton leaves, depth 2, 5 iterations).  Labels are stored
+    """Upstream MultiClassOneVsAll, MultiLogloss, MultiCrossEntropy and
+    RMSEWithUncertainty fixtures on numeric_tiny (Newton leaves).  Labels are stored
     as the dim-major [K, n] matrix each fit consumes: OneVsAll's one-hot of the
     digitized classes (the multiclass_softmax rule); for the two label losses
     the nested thresholds y > quantile(y, [.25, .5, .75]) that the reference's
@@ -262,13 +262,15 @@ def multi_output_fixtures(ref):
     y = np.load(os.path.join(fx, "inputs/numeric_tiny/y.npy"))
     n = X.shape[0]
     out = {"X": X.astype(np.float32)}
-    for sc in ("multiclass_onevsall", "multilogloss", "multicrossentropy"):
+    for sc in ("multiclass_onevsall", "multilogloss", "multicrossentropy", "rmse_uncertainty"):
         cfg = json.loads(_read(os.path.join(fx, sc, "config.json")))
         model = json.loads(_read(os.path.join(fx, sc, "model.json")))
         K = int(cfg["approx_dimension"])
         if sc == "multiclass_onevsall":
             cls = np.digitize(y, np.quantile(y, [1 / 3, 2 / 3]))
             labels = (np.arange(K)[:, None] == cls[None, :]).astype(np.float64)
+        elif sc == "rmse_uncertainty":  # the raw target; K = 2 is [mean, log-scale]
+            labels = y[None, :].astype(np.float64)
         else:
             labels = np.vstack([y > np.quantile(y, q) for q in (0.25, 0.5, 0.75)]).astype(np.float64)
         trees = model["oblivious_trees"]
