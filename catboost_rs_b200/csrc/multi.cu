@@ -159,6 +159,17 @@ __global__ void mc_der_kernel(int64_t n, int K, double* __restrict__ approx, con
         }
         const double w = weight ? weight[i] : 1.0;
         bool finite = true;
+        if (diag == 2) {
+            // rmse_with_uncertainty_ders (loss.rs:680-720): [w diff, w (diff^2 prec - 1)]
+            const double diff = __dsub_rn(tmat[i], approx[i]);
+            const double prec = exp(__dmul_rn(-2.0, approx[(size_t)n + i]));
+            const double dsp = __dmul_rn(__dmul_rn(diff, diff), prec);
+            const double v0 = __dmul_rn(w, diff), v1 = __dmul_rn(w, __dsub_rn(dsp, 1.0));
+            wd1[i] = v0;
+            wd1[(size_t)n + i] = v1;
+            if (!(isfinite(v0) && isfinite(v1))) atomicOr(&ms->err, kMcErrNonFinite);
+            continue;
+        }
         if (diag) {
             const int y = tmat ? -1 : target[i];
             for (int d = 0; d < K; ++d) {
@@ -407,8 +418,12 @@ __global__ void mc_route_kernel(int64_t n, int level, const uint8_t* __restrict_
 // (the per-dimension scalar sums of boosting.rs:8323-8420).
 __global__ void __launch_bounds__(kMcThreads)
 mc_leafsum_kernel(int64_t n, int K, int L, const double* __restrict__ approx, const double* __restrict__ wd1,
-                  const double* __restrict__ weight, const uint16_t* __restrict__ leaf, int leaf_shift, int diag,
-                  unsigned long long* __restrict__ sums, int use_smem, McState* __restrict__ ms) {
+                  const double* __restrict__ weight, const uint16_t* __restrict__ leaf, int leaf_shift_in, int diag,
+                  const double* __restrict__ tmat, unsigned long long* __restrict__ sums, int use_smem,
+                  McState* __restrict__ ms) {
+    // RMSEWithUncertainty's ders are unbounded: its sums take the tree's score
+    // shift less 2 (|w der2| <= 2 |w der1_1| + 2 w <= 4 max channel)
+    const int leaf_shift = diag == 2 ? ms->hist_shift - 2 : leaf_shift_in;
     extern __shared__ unsigned long long ltab[];
     const int pk = K * (K + 1) / 2, W = K + pk;
     if (use_smem) {
@@ -427,6 +442,14 @@ mc_leafsum_kernel(int64_t n, int K, int L, const double* __restrict__ approx, co
         for (int d = 0; d < K; ++d)
             atomicAdd(&cell[d], (unsigned long long)llrint(ldexp(wd1[(size_t)d * n + i], leaf_shift)));
         const double w = weight ? weight[i] : 1.0;
+        if (diag == 2) {
+            const double diff = __dsub_rn(tmat[i], approx[i]);
+            const double prec = exp(__dmul_rn(-2.0, approx[(size_t)n + i]));
+            const double dsp = __dmul_rn(__dmul_rn(diff, diff), prec);
+            atomicAdd(&cell[K], (unsigned long long)llrint(ldexp(-w, leaf_shift)));
+            atomicAdd(&cell[K + 1], (unsigned long long)llrint(ldexp(__dmul_rn(__dmul_rn(-2.0, w), dsp), leaf_shift)));
+            continue;
+        }
         if (diag) {
             for (int d = 0; d < K; ++d) {
                 const double pd = mc_sigmoid(approx[(size_t)d * n + i]);
@@ -458,11 +481,12 @@ mc_leafsum_kernel(int64_t n, int K, int L, const double* __restrict__ approx, co
 // zeros on a non-positive pivot; delta x lr for the approximant.
 // Diagonal losses: newton_leaf_delta per dimension (leaf.rs:196-232),
 // s1 / (-s2 + l2), 0 on a zero denominator.
-__global__ void mc_newton_kernel(int K, int L, const unsigned long long* __restrict__ sums, int leaf_shift,
-                                 double l2, double lr, int diag, double* __restrict__ leaf_raw,
-                                 double* __restrict__ leaf_lrv) {
+__global__ void mc_newton_kernel(int K, int L, const unsigned long long* __restrict__ sums, int leaf_shift_in,
+                                 double l2, double lr, int diag, const McState* __restrict__ ms,
+                                 double* __restrict__ leaf_raw, double* __restrict__ leaf_lrv) {
     const int q = blockIdx.x * blockDim.x + threadIdx.x;
     if (q >= L) return;
+    const int leaf_shift = diag == 2 ? ms->hist_shift - 2 : leaf_shift_in;
     const int pk = K * (K + 1) / 2, W = K + pk;
     const double inv = ldexp(1.0, -leaf_shift);
     if (diag) {
@@ -529,6 +553,13 @@ __global__ void mc_newton_kernel(int K, int L, const unsigned long long* __restr
         const double delta = ok ? -x[d] : 0.0;
         leaf_raw[(size_t)q * K + d] = delta;                 // leaf-major, raw (the seam's layout)
         leaf_lrv[(size_t)d * L + q] = __dmul_rn(delta, lr);  // dim-major, x lr (normalize_leaf_values)
+    }
+}
+
+__global__ void mc_fill2_kernel(int64_t n, double* __restrict__ approx, double b0, double b1) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        approx[i] = b0;
+        approx[(size_t)n + i] = b1;
     }
 }
 
@@ -1578,8 +1609,10 @@ int begin_impl(const cbgpu_begin_args* a, int32_t K, const float* const* cols, c
     s->F0 = a->n_features;
     s->F = a->n_features + n_cat;
     s->loss = a->loss;
-    s->diag = a->loss == CBGPU_LOSS_MULTICLASS_ONE_VS_ALL || a->loss == CBGPU_LOSS_MULTILOGLOSS ||
-              a->loss == CBGPU_LOSS_MULTICROSSENTROPY;
+    s->diag = a->loss == CBGPU_LOSS_RMSE_WITH_UNCERTAINTY
+                  ? 2
+                  : (a->loss == CBGPU_LOSS_MULTICLASS_ONE_VS_ALL || a->loss == CBGPU_LOSS_MULTILOGLOSS ||
+                     a->loss == CBGPU_LOSS_MULTICROSSENTROPY);
     s->score_fn = a->score_function;
     s->boot = a->bootstrap_type;
     s->sample_from_host = a->sample_from_host;
@@ -1627,6 +1660,7 @@ int begin_impl(const cbgpu_begin_args* a, int32_t K, const float* const* cols, c
     MDA(s->q, (size_t)C * n);
     MDA(s->target, n);
     if (a->loss == CBGPU_LOSS_MULTILOGLOSS || a->loss == CBGPU_LOSS_MULTICROSSENTROPY) MDA(s->d_tmat, (size_t)K * n);
+    if (a->loss == CBGPU_LOSS_RMSE_WITH_UNCERTAINTY) MDA(s->d_tmat, n);
     MDA(s->leaf, n);
     MDA(s->sw32, n);
     MDA(s->sw64, n);
@@ -1718,8 +1752,12 @@ int cbgpu_multi_begin_cat_raw(const cbgpu_begin_args* a, int32_t approx_dim, con
     }
     // the coverage this arm accepts; everything else declines to the CPU grower
     const bool labels = a->loss == CBGPU_LOSS_MULTILOGLOSS || a->loss == CBGPU_LOSS_MULTICROSSENTROPY;
-    if (a->loss != CBGPU_LOSS_MULTICLASS && a->loss != CBGPU_LOSS_MULTICLASS_ONE_VS_ALL && !labels)
+    const bool uncertainty = a->loss == CBGPU_LOSS_RMSE_WITH_UNCERTAINTY;
+    if (a->loss != CBGPU_LOSS_MULTICLASS && a->loss != CBGPU_LOSS_MULTICLASS_ONE_VS_ALL && !labels && !uncertainty)
         return mfail(CBGPU_DECLINED, "multi_begin: loss %d is not a covered multi-output loss", a->loss);
+    // its leaf sums take the tree's score shift, which a bootstrap sample would shrink
+    if (uncertainty && (approx_dim != 2 || a->bootstrap_type != CBGPU_BOOT_NO || a->sample_from_host))
+        return mfail(CBGPU_DECLINED, "multi_begin: RMSEWithUncertainty needs approx_dim 2 and bootstrap No");
     if (a->grow_policy != CBGPU_GROW_SYMMETRIC || !a->boosting_type_is_plain || a->fold_count != 1)
         return mfail(CBGPU_DECLINED, "multi_begin: only Plain SymmetricTree with one fold");
     if (a->score_function != CBGPU_SCORE_COSINE && a->score_function != CBGPU_SCORE_L2 &&
@@ -2093,6 +2131,26 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
         MCU(cudaStreamSynchronize(st));
         s->target_ready = true;
     }
+    if (!s->target_ready && s->diag == 2) {
+        if (!target) return mfail(CBGPU_ERR_INVALID, "multi_grow: the first call needs the target");
+        for (int64_t i = 0; i < n; ++i)
+            if (!std::isfinite(target[i]))
+                return mfail(CBGPU_ERR_INVALID, "multi_grow: target %g at row %lld is not finite", target[i],
+                             (long long)i);
+        // the starting approximant [f32 mean, 0.5 ln f32 var] (boosting.rs:1895-1914)
+        double acc = 0.0;
+        for (int64_t i = 0; i < n; ++i) acc += target[i];
+        const double mean = (double)(float)(acc / (double)n);
+        double sq = 0.0;
+        for (int64_t i = 0; i < n; ++i) sq += (target[i] - mean) * (target[i] - mean);
+        const double log_scale = 0.5 * std::log((double)(float)(sq / (double)n));
+        MCU(cudaMemcpyAsync(s->d_tmat, target, sizeof(double) * n, cudaMemcpyHostToDevice, st));
+        mc_fill2_kernel<<<(unsigned)std::min<int64_t>((n + kMcThreads - 1) / kMcThreads, 148 * 8), kMcThreads, 0,
+                          st>>>(n, s->approx, mean, log_scale);
+        MCU(cudaGetLastError());
+        MCU(cudaStreamSynchronize(st));
+        s->target_ready = true;
+    }
     if (!s->target_ready && s->d_tmat) {
         // MultiLogloss {0, 1} / MultiCrossEntropy [0, 1] labels (Loss::validate)
         if (!target) return mfail(CBGPU_ERR_INVALID, "multi_grow: the first call needs the target");
@@ -2330,8 +2388,9 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
         if (luse && ltab > 48 * 1024)
             MCU(cudaFuncSetAttribute(mc_leafsum_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ltab));
         mc_leafsum_kernel<<<g, kMcThreads, luse ? ltab : 0, st>>>(n, K, L, s->approx, s->wd1, s->weight, s->leaf,
-                                                                 s->leaf_shift, s->diag, s->sums, luse, s->d_ms);
-        mc_newton_kernel<<<(L + 63) / 64, 64, 0, st>>>(K, L, s->sums, s->leaf_shift, s->l2, s->lr, s->diag,
+                                                                 s->leaf_shift, s->diag, s->d_tmat, s->sums, luse,
+                                                                 s->d_ms);
+        mc_newton_kernel<<<(L + 63) / 64, 64, 0, st>>>(K, L, s->sums, s->leaf_shift, s->l2, s->lr, s->diag, s->d_ms,
                                                        s->leaf_raw, s->leaf_lrv);
         MCU(cudaGetLastError());
     }

@@ -21,7 +21,8 @@ from . import _lib
 LOSS = {"RMSE": 0, "Rmse": 0, "Logloss": 1, "CrossEntropy": 2, "MultiClass": 3, "QueryRMSE": 4, "PairLogit": 5,
         "PairLogitPairwise": 6, "QuerySoftMax": 7,
         "LambdaMart": 8, "YetiRank": 9, "StochasticRank": 10, "YetiRankPairwise": 11, "MultiClassOneVsAll": 12,
-        "MultiLogloss": 13, "MultiCrossEntropy": 14, "MAE": 15, "Quantile": 16}
+        "MultiLogloss": 13, "MultiCrossEntropy": 14, "MAE": 15, "Quantile": 16,
+        "RMSEWithUncertainty": 17}
 # multi-output losses whose target is the [K, n] label matrix (dim-major)
 LABEL_MATRIX_LOSSES = ("MultiLogloss", "MultiCrossEntropy")
 LAMBDAMART_METRIC = {"NDCG": 0, "DCG": 1, "MRR": 2, "ERR": 3, "MAP": 4}

@@ -55,7 +55,8 @@ typedef enum {
     CBGPU_LOSS_QUERYSOFTMAX = 7, CBGPU_LOSS_LAMBDAMART = 8, CBGPU_LOSS_YETIRANK = 9,
     CBGPU_LOSS_STOCHASTICRANK = 10, CBGPU_LOSS_YETIRANK_PAIRWISE = 11,
     CBGPU_LOSS_MULTICLASS_ONE_VS_ALL = 12, CBGPU_LOSS_MULTILOGLOSS = 13, CBGPU_LOSS_MULTICROSSENTROPY = 14,
-    CBGPU_LOSS_MAE = 15, CBGPU_LOSS_QUANTILE = 16  /* the scalar session, Exact leaves only */
+    CBGPU_LOSS_MAE = 15, CBGPU_LOSS_QUANTILE = 16, /* the scalar session, Exact leaves only */
+    CBGPU_LOSS_RMSE_WITH_UNCERTAINTY = 17          /* the multi-output session, approx_dim 2 */
 } cbgpu_loss;
 
 /* EScoreFunction (runtime.rs:834-864); Cosine is the default. */
@@ -309,7 +310,9 @@ CBGPU_API int cbgpu_multi_begin_cat_raw(const cbgpu_begin_args* args, int32_t ap
  *            (0..K-1) for MultiClass and MultiClassOneVsAll; for MultiLogloss
  *            ({0, 1}) and MultiCrossEntropy ([0, 1]) the [K * n] DIM-major
  *            label matrix target[d * n + i], the reference's multilabel
- *            layout;
+ *            layout; for RMSEWithUncertainty the [n] targets, and the
+ *            approximant then starts at [f32 mean, 0.5 ln f32 variance]
+ *            (boosting.rs:1895-1914);
  *  sample    the host bootstrap multiplier, as for cbgpu_grow_tree;
  *  leaf_values [2^depth * K] LEAF-major raw deltas (DeviceGrownTree's
  *            leaf_count x approx_dim block, runtime.rs:1008-1024), not scaled

@@ -5,8 +5,11 @@ device arm (csrc/multi.cu): per dimension p = sigmoid(a_d), der1 = t_d - p,
 der2 = -p (1 - p) (crates/cb-compute/src/loss.rs:501-560), K + 1 channel
 histograms scored by the multi-dimensional score, and each dimension's Newton
 leaf s1 / (-s2 + l2) solved on its own (crates/cb-train/src/boosting.rs:
-8323-8420).  Trees must match the oracle's; leaf values and staged
-approximants within the reference's 1e-5 bar.
+8323-8420).  RMSEWithUncertainty shares the diagonal leaf with its own ders
+(loss.rs:680-720), leaf sums at the tree's score shift less 2 (its ders are
+unbounded), and the starting approximant [f32 mean, 0.5 ln f32 var]
+(boosting.rs:1895-1914).  Trees must match the oracle's; leaf values and
+staged approximants within the reference's 1e-5 bar.
 """
 import json
 import os
@@ -40,7 +43,7 @@ def _fp(cb, **kw):
     return cb.FitParams(**base)
 
 
-@pytest.mark.parametrize("sc", ["multiclass_onevsall", "multilogloss", "multicrossentropy"])
+@pytest.mark.parametrize("sc", ["multiclass_onevsall", "multilogloss", "multicrossentropy", "rmse_uncertainty"])
 def test_multi_output_fixture(cb, sc):
     z = np.load(GOLDEN)
     p = json.loads(str(z[f"{sc}__params"]))
@@ -49,7 +52,8 @@ def test_multi_output_fixture(cb, sc):
     fp = _fp(cb, depth=p["depth"], iterations=p["iterations"], learning_rate=p["learning_rate"],
              l2_leaf_reg=p["l2_leaf_reg"], score_function=p["score_function"])
     labels = z[f"{sc}__labels"]
-    target = np.argmax(labels, axis=0) if p["loss"] == "MultiClassOneVsAll" else labels
+    target = {"MultiClassOneVsAll": lambda: np.argmax(labels, axis=0),
+              "RMSEWithUncertainty": lambda: labels[0]}.get(p["loss"], lambda: labels)()
     m = cb.fit_multiclass([X[:, f].copy() for f in range(X.shape[1])], borders, target, p["approx_dimension"], fp,
                           staged=True, loss=p["loss"])
     np.testing.assert_array_equal(m.split_feature, z[f"{sc}__split_feature"])
@@ -65,6 +69,8 @@ CASES = [
     dict(loss="MultiLogloss", n=70001, F=5, K=2, depth=8, boot="No", score="Cosine", it=3, w=False),
     dict(loss="MultiCrossEntropy", n=15000, F=8, K=5, depth=4, boot="No", score="Cosine", it=5, w=False),
     dict(loss="MultiCrossEntropy", n=8000, F=6, K=1, depth=4, boot="Bernoulli", score="L2", it=4, w=True),
+    dict(loss="RMSEWithUncertainty", n=25000, F=8, K=2, depth=6, boot="No", score="L2", it=6, w=False),
+    dict(loss="RMSEWithUncertainty", n=7000, F=5, K=2, depth=4, boot="No", score="Cosine", it=5, w=True),
 ]
 
 
@@ -76,6 +82,8 @@ def _data(case):
     lin = np.nan_to_num(X[:, :min(F, max(K, 2))]) @ rs.standard_normal((min(F, max(K, 2)), K))
     if case["loss"] == "MultiClassOneVsAll":
         target = np.argmax(lin + rs.gumbel(size=(n, K)), axis=1).astype(np.int32)
+    elif case["loss"] == "RMSEWithUncertainty":  # heteroscedastic: the noise grows with feature 1
+        target = lin[:, 0] + np.exp(0.5 * np.nan_to_num(X[:, 1])) * rs.standard_normal(n)
     elif case["loss"] == "MultiLogloss":
         target = (lin + rs.logistic(size=(n, K)) > 0).T.astype(np.float64)
     else:  # soft labels in [0, 1], the two ends included
