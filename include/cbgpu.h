@@ -276,7 +276,9 @@ CBGPU_API int cbgpu_histogram_noalloc(const uint8_t* d_bins_row_major, int64_t n
  * (loss.rs:501-560) share the arm: per dimension p = sigmoid(a_d),
  * der1 = t_d - p, der2 = -p (1 - p), and each dimension's Newton leaf is
  * solved on its own (boosting.rs:8323-8420) instead of the coupled softmax
- * solve.
+ * solve.  RMSEWithUncertainty (loss.rs:680-720; approx_dim 2, bootstrap No)
+ * takes the same per-dimension leaf with der1 = w [diff, diff^2 prec - 1],
+ * der2 = w [-1, -2 diff^2 prec], diff = t - a0, prec = exp(-2 a1).
  *
  * cbgpu_multi_begin_raw: begin_device_training_raw's arguments (loss one of
  * CBGPU_LOSS_MULTICLASS, _MULTICLASS_ONE_VS_ALL, _MULTILOGLOSS,
