@@ -58,3 +58,17 @@ def test_begin_args_layout_matches_header():
     body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)
     fields = re.findall(r"\b(\w+);", body)
     assert [f for f, _ in BeginArgs._fields_] == fields
+
+
+def test_loss_ids_match_the_header():
+    # every cbgpu_loss enumerator and the host map agree, so a new loss id
+    # cannot drift between include/cbgpu.h and the Python mirror
+    from catboost_rs_b200 import runtime
+    hdr = open(os.path.join(os.path.dirname(os.path.abspath(__file__)), "..", "include", "cbgpu.h")).read()
+    body = hdr[hdr.index("CBGPU_LOSS_RMSE = 0"):hdr.index("} cbgpu_loss;")]
+    ids = {k: int(v) for k, v in re.findall(r"CBGPU_LOSS_(\w+)\s*=\s*(\d+)", body)}
+    norm = lambda s: s.upper().replace("_", "")  # noqa: E731
+    by_name = {norm(k): v for k, v in ids.items()}
+    for name, v in runtime.LOSS.items():
+        assert by_name.get(norm(name)) == v, name
+    assert set(ids.values()) <= set(runtime.LOSS.values())
