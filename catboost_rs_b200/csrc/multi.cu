@@ -113,8 +113,6 @@ struct McState {
     uint32_t pad;
     unsigned long long maxbits;  // bit pattern of max |score channel| (a non-negative double)
     int32_t hist_shift;          // score channels are llrint(v * 2^hist_shift)
-    int32_t leaf_shift;          // ranking mode: leaf sums are llrint(v * 2^leaf_shift)
-    unsigned long long lmaxbits; // ranking mode: max |der1|, |der2|, |w| bit pattern
 };
 
 // ---- kernels ---------------------------------------------------------------
@@ -752,51 +750,85 @@ __global__ void rk_der_kernel(int n_groups, int mode, const int64_t* __restrict_
     if (!finite) atomicOr(&ms->err, kMcErrNonFinite);
 }
 
-// max |der1|, |der2|, |w| of the tree -> leaf_shift (sums over n rows < 2^62)
-__global__ void rk_leafmax_kernel(int64_t n, const double* __restrict__ d1, const double* __restrict__ d2,
-                                  const double* __restrict__ weight, McState* __restrict__ ms) {
-    double mx = 1.0;  // the unit leaf weights Gradient leaves count
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
-        mx = fmax(mx, fmax(fabs(d1[i]), fmax(fabs(d2[i]), fabs(weight ? weight[i] : 1.0))));
-    for (int o = 16; o > 0; o >>= 1) mx = fmax(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    if ((threadIdx.x & 31) == 0 && mx > 0.0) atomicMax(&ms->lmaxbits, (unsigned long long)__double_as_longlong(mx));
-}
-
-__global__ void rk_leafshift_kernel(int64_t n, McState* ms) {
-    const double mx = __longlong_as_double((long long)ms->lmaxbits);
-    int e = 0;
-    if (mx > 0.0) frexp(mx, &e);
-    int t = 0;
-    while (t < 62 && (1ll << t) < n) ++t;
-    int sh = 61 - e - t;
-    if (sh > 1000) sh = 1000;
-    ms->leaf_shift = sh;
-}
-
-// Per-leaf int64 sums of der1, der2 (unit leaf weights for Newton,
-// boosting.rs:8345-8380) -- or, for Gradient leaves (count = 1), the row
-// count -- and the object weight (normalize_leaf_values' leaf weights,
-// boosting.rs:8525-8540): sums[leaf][3].
-__global__ void rk_leafsum_kernel(int64_t n, int L, const double* __restrict__ d1, const double* __restrict__ d2,
-                                  const double* __restrict__ weight, const uint16_t* __restrict__ leaf, int count,
-                                  unsigned long long* __restrict__ sums, McState* __restrict__ ms) {
-    __shared__ unsigned long long t3[3 * (1 << kMcMaxDepth)];
-    for (int k = threadIdx.x; k < 3 * L; k += blockDim.x) t3[k] = 0ull;
-    __syncthreads();
-    const int sh = ms->leaf_shift;
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-        const int q = leaf[i];
-        if (q >= L) {
-            atomicOr(&ms->err, kMcErrLeafRange);
-            continue;
+// Per-leaf sums of der1, der2 (unit leaf weights for Newton, boosting.rs:
+// 8345-8380) -- or, for Gradient leaves (count = 1), the row count -- and of
+// the object weight (normalize_leaf_values' leaf weights, boosting.rs:
+// 8525-8540): sums[leaf][3], each accumulated in f64 in object order exactly
+// as the CPU's `sum[leaf[i]] += v[i]` loop does, so the leaf values round as
+// the CPU's.  Grouped ders are discontinuous where two approximants tie
+// (LambdaMart's stable sort and its `same` rule), and the CPU keeps exact
+// cross-leaf ties (a leaf of only winners gets exactly -2 x the Hessian sum
+// as its der1 sum); a sum rounded any other way can split such a tie.
+// One block per leaf: each step compacts the leaf's members of 1024
+// consecutive rows into shared memory in row order (block scan of the
+// per-thread counts); thread 0 then runs the three sequential chains.
+constexpr int kSeqThreads = 256, kSeqRows = 4;
+__global__ void __launch_bounds__(kSeqThreads)
+rk_leafsum_seq_kernel(int64_t n, int L, const double* __restrict__ d1, const double* __restrict__ d2,
+                      const double* __restrict__ weight, const uint16_t* __restrict__ leaf, int count,
+                      double* __restrict__ sums, McState* __restrict__ ms) {
+    constexpr int kStep = kSeqThreads * kSeqRows;
+    __shared__ double v1[kStep], v2[kStep], v3[kStep];
+    __shared__ int wsum[kSeqThreads / 32 + 1];
+    const int q = blockIdx.x, tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    double s1 = 0.0, s2 = 0.0, s3 = 0.0;
+    bool bad = false;
+    for (int64_t base = 0; base < n; base += kStep) {
+        const int64_t r0 = base + (int64_t)tid * kSeqRows;
+        uint32_t lq[kSeqRows];
+#pragma unroll
+        for (int j = 0; j < kSeqRows; ++j) lq[j] = r0 + j < n ? leaf[r0 + j] : 0xffffu;
+        int m = 0;
+#pragma unroll
+        for (int j = 0; j < kSeqRows; ++j) {
+            m += lq[j] == (uint32_t)q ? 1 : 0;
+            bad |= lq[j] != 0xffffu && lq[j] >= (uint32_t)L;
         }
-        atomicAdd(&t3[3 * q], (unsigned long long)llrint(ldexp(d1[i], sh)));
-        atomicAdd(&t3[3 * q + 1], (unsigned long long)llrint(ldexp(count ? 1.0 : d2[i], sh)));
-        atomicAdd(&t3[3 * q + 2], (unsigned long long)llrint(ldexp(weight ? weight[i] : 1.0, sh)));
+        int inc = m;  // inclusive warp scan, then the warp offsets
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int t = __shfl_up_sync(0xffffffffu, inc, o);
+            if (lane >= o) inc += t;
+        }
+        if (lane == 31) wsum[wid] = inc;
+        __syncthreads();
+        if (tid == 0) {
+            int acc = 0;
+            for (int w = 0; w < kSeqThreads / 32; ++w) {
+                const int t = wsum[w];
+                wsum[w] = acc;
+                acc += t;
+            }
+            wsum[kSeqThreads / 32] = acc;
+        }
+        __syncthreads();
+        int pos = wsum[wid] + inc - m;
+#pragma unroll
+        for (int j = 0; j < kSeqRows; ++j)
+            if (lq[j] == (uint32_t)q) {
+                const int64_t i = r0 + j;
+                v1[pos] = d1[i];
+                v2[pos] = count ? 1.0 : __dmul_rn(d2[i], 1.0);
+                v3[pos] = weight ? weight[i] : 1.0;
+                ++pos;
+            }
+        __syncthreads();
+        if (tid == 0) {
+            const int tot = wsum[kSeqThreads / 32];
+            for (int k = 0; k < tot; ++k) {
+                s1 = __dadd_rn(s1, v1[k]);
+                s2 = __dadd_rn(s2, v2[k]);
+                s3 = __dadd_rn(s3, v3[k]);
+            }
+        }
+        __syncthreads();
     }
-    __syncthreads();
-    for (int k = threadIdx.x; k < 3 * L; k += blockDim.x)
-        if (t3[k]) atomicAdd(&sums[k], t3[k]);
+    if (bad) atomicOr(&ms->err, kMcErrLeafRange);
+    if (tid == 0) {
+        sums[3 * q] = s1;
+        sums[3 * q + 1] = s2;
+        sums[3 * q + 2] = s3;
+    }
 }
 
 // Newton leaves sum(der1) / (-sum(der2) + scaled_l2) (leaf.rs:223-232), or
@@ -804,14 +836,12 @@ __global__ void rk_leafsum_kernel(int64_t n, int L, const double* __restrict__ d
 // leaf.rs:161-194); the raw deltas go back through the seam; the approximant
 // gets normalize_leaf_values' result (PairLogit: minus the document-weighted
 // mean, boosting.rs:2844-2880) x lr.  One thread: L <= 1024 leaves.
-__global__ void rk_newton_kernel(int L, int pairwise, int gradient, const unsigned long long* __restrict__ sums,
-                                 const McState* __restrict__ ms, double l2, double lr, double* __restrict__ leaf_raw,
-                                 double* __restrict__ leaf_lrv) {
+__global__ void rk_newton_kernel(int L, int pairwise, int gradient, const double* __restrict__ sums, double l2,
+                                 double lr, double* __restrict__ leaf_raw, double* __restrict__ leaf_lrv) {
     if (blockIdx.x != 0 || threadIdx.x != 0) return;
-    const double inv = ldexp(1.0, -ms->leaf_shift);
     for (int q = 0; q < L; ++q) {
-        const double s1 = __dmul_rn((double)(long long)sums[3 * q], inv);
-        const double s2 = __dmul_rn((double)(long long)sums[3 * q + 1], inv);
+        const double s1 = sums[3 * q];
+        const double s2 = sums[3 * q + 1];
         if (gradient) {
             leaf_raw[q] = s2 > 0.0 ? __ddiv_rn(s1, __dadd_rn(s2, l2)) : 0.0;
         } else {
@@ -823,11 +853,10 @@ __global__ void rk_newton_kernel(int L, int pairwise, int gradient, const unsign
     bool centre = false;
     if (pairwise) {
         double total = 0.0;
-        for (int q = 0; q < L; ++q) total = __dadd_rn(total, __dmul_rn((double)(long long)sums[3 * q + 2], inv));
+        for (int q = 0; q < L; ++q) total = __dadd_rn(total, sums[3 * q + 2]);
         if (fabs(total) > 1e-9) {
             double acc = 0.0;
-            for (int q = 0; q < L; ++q)
-                acc = __dadd_rn(acc, __dmul_rn(leaf_raw[q], __dmul_rn((double)(long long)sums[3 * q + 2], inv)));
+            for (int q = 0; q < L; ++q) acc = __dadd_rn(acc, __dmul_rn(leaf_raw[q], sums[3 * q + 2]));
             avg = __ddiv_rn(acc, total);
             centre = true;
         }
@@ -835,7 +864,7 @@ __global__ void rk_newton_kernel(int L, int pairwise, int gradient, const unsign
     for (int q = 0; q < L; ++q) {
         double v = leaf_raw[q];
         if (centre) {
-            const double w = __dmul_rn((double)(long long)sums[3 * q + 2], inv);
+            const double w = sums[3 * q + 2];
             v = fabs(w) > 1e-9 ? __dsub_rn(v, avg) : 0.0;
         }
         leaf_lrv[q] = __dmul_rn(v, lr);
@@ -1406,17 +1435,16 @@ __global__ void rk_yeti_pairleafw_kernel(int n_groups, const int64_t* __restrict
 }
 
 // Cholesky pairwise leaves (compute_pairwise_leaf_deltas, pairwise_leaves.rs:
-// 219-242) from the leaf der sums (rk_leafsum_kernel's channel 0) with the raw
+// 219-242) from the leaf der sums (rk_leafsum_seq_kernel's channel 0) with the raw
 // l2, one block; the seam gets these deltas, the approximant
 // normalize_leaf_values' document-weighted centring x lr (boosting.rs:
 // 2844-2880).  scratch: pw_scratch_doubles(L).
 __global__ void __launch_bounds__(kPwThreads)
-rk_pairleaf_kernel(int L, const long long* __restrict__ wsum, const unsigned long long* __restrict__ sums,
-                   const McState* __restrict__ ms, double l2, double lr, int pw_shift, int centre_on,
-                   double* __restrict__ scratch, double* __restrict__ leaf_raw, double* __restrict__ leaf_lrv) {
+rk_pairleaf_kernel(int L, const long long* __restrict__ wsum, const double* __restrict__ sums, double l2, double lr,
+                   int pw_shift, int centre_on, double* __restrict__ scratch, double* __restrict__ leaf_raw,
+                   double* __restrict__ leaf_lrv) {
     __shared__ int s_flag;
     const int m = L - 1, tid = threadIdx.x;
-    const double inv = ldexp(1.0, -ms->leaf_shift);
     const double winv = ldexp(1.0, -pw_shift);
     double* w = scratch;
     double* A = w + (size_t)L * L;
@@ -1424,24 +1452,23 @@ rk_pairleaf_kernel(int L, const long long* __restrict__ wsum, const unsigned lon
     double* y = der + L;
     double* x = y + L;
     for (int k = tid; k < L * L; k += blockDim.x) w[k] = __dmul_rn((double)wsum[k], winv);
-    for (int q = tid; q < L; q += blockDim.x) der[q] = __dmul_rn((double)(long long)sums[3 * q], inv);
+    for (int q = tid; q < L; q += blockDim.x) der[q] = sums[3 * q];
     __syncthreads();
     pw_leaf_values_block(w, der, L, l2, leaf_raw, A, y, x, &s_flag);
     if (tid != 0) return;
     double total = 0.0;
-    for (int q = 0; q < L; ++q) total = __dadd_rn(total, __dmul_rn((double)(long long)sums[3 * q + 2], inv));
+    for (int q = 0; q < L; ++q) total = __dadd_rn(total, sums[3 * q + 2]);
     double avg = 0.0;
     const bool centre = centre_on && fabs(total) > 1e-9;
     if (centre) {
         double acc = 0.0;
-        for (int q = 0; q < L; ++q)
-            acc = __dadd_rn(acc, __dmul_rn(leaf_raw[q], __dmul_rn((double)(long long)sums[3 * q + 2], inv)));
+        for (int q = 0; q < L; ++q) acc = __dadd_rn(acc, __dmul_rn(leaf_raw[q], sums[3 * q + 2]));
         avg = __ddiv_rn(acc, total);
     }
     for (int q = 0; q < L; ++q) {
         double v = leaf_raw[q];
         if (centre) {
-            const double wq = __dmul_rn((double)(long long)sums[3 * q + 2], inv);
+            const double wq = sums[3 * q + 2];
             v = fabs(wq) > 1e-9 ? __dsub_rn(v, avg) : 0.0;
         }
         leaf_lrv[q] = __dmul_rn(v, lr);
@@ -2335,11 +2362,9 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
                                                s->d_lmden, s->d_lmideal, s->d_srank_ws, s->d_lmorder, s->wd1,
                                                s->d_der2, s->d_ms);
         const int gradient = (s->rank_mode == kRankQuerySoftMax || srank) ? 1 : 0;
-        rk_leafmax_kernel<<<g, kMcThreads, 0, st>>>(n, s->wd1, s->d_der2, s->weight, s->d_ms);
-        rk_leafshift_kernel<<<1, 1, 0, st>>>(n, s->d_ms);
-        MCU(cudaMemsetAsync(s->sums, 0, sizeof(unsigned long long) * 3 * (size_t)L, st));
-        rk_leafsum_kernel<<<g, kMcThreads, 0, st>>>(n, L, s->wd1, s->d_der2, s->weight, s->leaf, gradient, s->sums,
-                                                    s->d_ms);
+        double* rsum = reinterpret_cast<double*>(s->sums);  // 3 f64 per leaf in the ranking mode
+        rk_leafsum_seq_kernel<<<L, kSeqThreads, 0, st>>>(n, L, s->wd1, s->d_der2, s->weight, s->leaf, gradient, rsum,
+                                                         s->d_ms);
         if (pairwise) {
             MCU(cudaMemsetAsync(s->d_pwsum, 0, sizeof(long long) * (size_t)L * L, st));
             if (yeti)
@@ -2348,11 +2373,11 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
             else
                 rk_pairleafw_kernel<<<grid_for(s->n_pairs), kMcThreads, 0, st>>>(
                     s->n_pairs, L, s->d_pwin, s->d_closer, s->leaf, s->pw_shift, s->d_pwsum);
-            rk_pairleaf_kernel<<<1, kPwThreads, 0, st>>>(L, s->d_pwsum, s->sums, s->d_ms, s->raw_l2, s->lr,
-                                                         s->pw_shift, 1, s->d_pwscratch, s->leaf_raw, s->leaf_lrv);
+            rk_pairleaf_kernel<<<1, kPwThreads, 0, st>>>(L, s->d_pwsum, rsum, s->raw_l2, s->lr, s->pw_shift, 1,
+                                                         s->d_pwscratch, s->leaf_raw, s->leaf_lrv);
         } else {
-            rk_newton_kernel<<<1, 1, 0, st>>>(L, (s->rank_mode == kRankPairLogit || yeti) ? 1 : 0, gradient, s->sums,
-                                              s->d_ms, s->l2, s->lr, s->leaf_raw, s->leaf_lrv);
+            rk_newton_kernel<<<1, 1, 0, st>>>(L, (s->rank_mode == kRankPairLogit || yeti) ? 1 : 0, gradient, rsum,
+                                              s->l2, s->lr, s->leaf_raw, s->leaf_lrv);
         }
         if (yeti) {
             // the learning fold: its own resample, Newton deltas x lr, no centring
@@ -2361,21 +2386,16 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
                                                      s->d_cw, s->d_lmorder, s->d_yboot);
             rk_yeti_der_kernel<<<yg, 128, 0, st>>>(s->n_groups, s->d_goff, s->d_lapprox, s->d_gw, s->yeti_perms,
                                                   s->d_cwoff, s->d_cw, s->wd1, s->d_der2, nullptr, s->d_ms);
-            rk_leafmax_kernel<<<g, kMcThreads, 0, st>>>(n, s->wd1, s->d_der2, s->weight, s->d_ms);
-            rk_leafshift_kernel<<<1, 1, 0, st>>>(n, s->d_ms);
-            MCU(cudaMemsetAsync(s->sums, 0, sizeof(unsigned long long) * 3 * (size_t)L, st));
-            rk_leafsum_kernel<<<g, kMcThreads, 0, st>>>(n, L, s->wd1, s->d_der2, s->weight, s->leaf, 0, s->sums,
-                                                        s->d_ms);
+            rk_leafsum_seq_kernel<<<L, kSeqThreads, 0, st>>>(n, L, s->wd1, s->d_der2, s->weight, s->leaf, 0, rsum,
+                                                             s->d_ms);
             if (pairwise) {  // YetiRankPairwise: Cholesky deltas for the learning fold too
                 MCU(cudaMemsetAsync(s->d_pwsum, 0, sizeof(long long) * (size_t)L * L, st));
                 rk_yeti_pairleafw_kernel<<<yg, 128, 0, st>>>(s->n_groups, s->d_goff, s->d_cwoff, s->d_cw, s->d_gw,
                                                             s->yeti_perms, L, s->leaf, s->pw_shift, s->d_pwsum);
-                rk_pairleaf_kernel<<<1, kPwThreads, 0, st>>>(L, s->d_pwsum, s->sums, s->d_ms, s->raw_l2, s->lr,
-                                                             s->pw_shift, 0, s->d_pwscratch, s->d_ylf_raw,
-                                                             s->d_ylf_lrv);
+                rk_pairleaf_kernel<<<1, kPwThreads, 0, st>>>(L, s->d_pwsum, rsum, s->raw_l2, s->lr, s->pw_shift, 0,
+                                                             s->d_pwscratch, s->d_ylf_raw, s->d_ylf_lrv);
             } else {
-                rk_newton_kernel<<<1, 1, 0, st>>>(L, 0, 0, s->sums, s->d_ms, s->l2, s->lr, s->d_ylf_raw,
-                                                  s->d_ylf_lrv);
+                rk_newton_kernel<<<1, 1, 0, st>>>(L, 0, 0, rsum, s->l2, s->lr, s->d_ylf_raw, s->d_ylf_lrv);
             }
             mc_apply_pending_kernel<<<g, kMcThreads, 0, st>>>(n, 1, L, s->d_lapprox, s->leaf, s->d_ylf_lrv);
         }
