@@ -77,15 +77,25 @@ def _block(b: int, F: int, seed: int):
 
 
 def make_shard(row_offset: int, n: int, F: int, seed: int):
+    """Rows [row_offset, row_offset + n) as features [F][n] f32 and labels; the
+    1Mi-row blocks are generated on a thread pool (each block has its own
+    seeded generator, so the rows do not depend on the thread count)."""
+    from concurrent.futures import ThreadPoolExecutor
     X = np.empty((F, n), dtype=np.float32)
     y = np.empty(n, dtype=np.float64)
     b0, b1 = row_offset // BLOCK_ROWS, (row_offset + n - 1) // BLOCK_ROWS
-    for b in range(b0, b1 + 1):
+
+    def fill(b):
         Xb, yb = _block(b, F, seed)
         lo = max(row_offset, b * BLOCK_ROWS)
         hi = min(row_offset + n, (b + 1) * BLOCK_ROWS)
         X[:, lo - row_offset:hi - row_offset] = Xb[:, lo - b * BLOCK_ROWS:hi - b * BLOCK_ROWS]
         y[lo - row_offset:hi - row_offset] = yb[lo - b * BLOCK_ROWS:hi - b * BLOCK_ROWS]
+
+    if n > 0:
+        workers = max(1, min(b1 - b0 + 1, os.cpu_count() or 1, 16))
+        with ThreadPoolExecutor(workers) as ex:
+            list(ex.map(fill, range(b0, b1 + 1)))
     return X, y
 
 
@@ -223,26 +233,29 @@ class ClockSampler:
 # CPU baseline / reference arm: the C restatement of the reference CPU path
 # ---------------------------------------------------------------------------
 
-def cpu_reference_run(args, n_sample: int, trees: int, warm: int):
+def cpu_reference_run(args, X, y, trees: int, warm: int, budget_s: float):
+    """The oracle (the C restatement of the reference CPU path, OpenMP over
+    features as the reference's rayon loop) on the FULL workload: every row
+    and feature, boosting trees at the config's depth, all host threads.
+    `warm` untimed trees first; then `trees` timed trees, fewer when the
+    warm-up tree's time says they would exceed `budget_s` (at least 3)."""
     from oracle import oracle as orc
-    F = args.features
-    X, y = make_shard(0, n_sample, F, args.seed)
-    borders = make_borders(F, args.border_count, args.seed)
+    borders = make_borders(args.features, args.border_count, args.seed)
     bins = orc.quantize(X, borders)
-    del X
     threads = os.cpu_count() or 1
     kw = dict(loss="Logloss", depth=args.depth, learning_rate=0.05, l2_leaf_reg=3.0,
               score_function="Cosine", bootstrap_type="Bayesian", bagging_temperature=1.0,
               random_seed=0, boost_from_average=False, staged=False, n_threads=threads)
+    counts = [len(b) for b in borders]
     if warm:
-        orc.train(bins, [len(b) for b in borders], y, iterations=warm, **kw)
+        t0 = time.perf_counter()
+        orc.train(bins, counts, y, iterations=warm, **kw)
+        per = (time.perf_counter() - t0) / warm
+        trees = max(3, min(trees, int(budget_s / max(per, 1e-9))))
     t0 = time.perf_counter()
-    orc.train(bins, [len(b) for b in borders], y, iterations=trees, **kw)
+    orc.train(bins, counts, y, iterations=trees, **kw)
     dt = time.perf_counter() - t0
-    per_tree_sample = dt / trees
-    # CPU cost per tree is linear in rows (every level visits every row per feature)
-    per_tree_full = per_tree_sample * (args.rows / n_sample)
-    return 1.0 / per_tree_full, threads, dt
+    return trees / dt, threads, dt, trees
 
 
 # ---------------------------------------------------------------------------
@@ -260,8 +273,8 @@ def main():
     ap.add_argument("--depth", type=int, default=8)
     ap.add_argument("--border-count", type=int, default=128)
     ap.add_argument("--seed", type=int, default=20261201)
-    ap.add_argument("--cpu-sample-rows", type=int, default=500_000)
-    ap.add_argument("--cpu-trees", type=int, default=2)
+    ap.add_argument("--cpu-trees", type=int, default=3)
+    ap.add_argument("--cpu-budget-s", type=float, default=60.0)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()
@@ -280,19 +293,19 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return
-        per = (args.steps + args.warmup)
-        # bounded sample: about a minute of CPU work for the whole run
-        sample = min(args.rows, args.cpu_sample_rows)
-        tps, cores, dt = cpu_reference_run(args, sample, args.steps, args.warmup)
+        # the full workload (every row and feature); the timed trees are bounded
+        # by a time budget so the run ends within a few minutes
+        X, y = make_shard(0, args.rows, args.features, args.seed)
+        tps, cores, dt, timed = cpu_reference_run(args, X, y, args.steps, 1, 2.0 * args.cpu_budget_s)
+        sample = (f"C restatement of the reference CPU path (oracle/), full workload {args.rows} rows x "
+                  f"{args.features} features at depth {args.depth}, {cores} threads: 1 warm-up tree, then "
+                  f"{timed} boosting trees timed ({dt:.1f} s); no extrapolation")
         line = {"impl": "reference", "metric": metric, "value": tps, "unit": "trees/s",
                 "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
                 "ms_per_step": 1e3 / tps, "higher_is_better": True, "scaling": "strong",
                 "vs_baseline": None, "dtype": "f64", "data": "synthetic", "config": base_cfg,
                 "cpu_baseline": {"value": tps, "unit": "trees/s", "cores": cores, "kind": "port",
-                                 "sample": f"C restatement of the reference CPU path (oracle/), {sample} rows x "
-                                           f"{args.features} features, {args.steps} timed trees after "
-                                           f"{args.warmup} warm-up; time per tree scaled by {args.rows}/{sample} "
-                                           f"(per-tree CPU cost is linear in rows)"},
+                                 "sample": sample, "timed_trees": timed},
                 "e2e": {"value": tps, "unit": "trees/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
         return
@@ -416,11 +429,12 @@ def main():
     # ---- CPU baseline (rank 0, N=1 only) -------------------------------------
     cpu = None
     if world == 1 and not args.no_cpu:
-        sample = min(args.rows, args.cpu_sample_rows)
-        tps, cores, dt = cpu_reference_run(args, sample, args.cpu_trees, 0)
+        del cols
+        tps, cores, dt, timed = cpu_reference_run(args, X, y, args.cpu_trees, 0, args.cpu_budget_s)
         cpu = {"value": tps, "unit": "trees/s", "cores": cores, "kind": "port",
-               "sample": f"C restatement of the reference CPU path (oracle/) on {sample} rows x {F} features, "
-                         f"{args.cpu_trees} trees ({dt:.1f} s), time per tree scaled by {args.rows}/{sample}"}
+               "sample": f"C restatement of the reference CPU path (oracle/) on the full workload "
+                         f"({n} rows x {F} features, depth {args.depth}), {timed} boosting trees timed "
+                         f"({dt:.1f} s, {cores} threads); no extrapolation"}
 
     if rank == 0:
         line = {"metric": metric, "value": value, "unit": "trees/s", "n_gpus": world, "steps": args.steps,

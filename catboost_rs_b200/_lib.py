@@ -45,6 +45,7 @@ EXPORTS = [
     "cbgpu_session_timing", "cbgpu_session_timing_sum", "cbgpu_session_set_profiling", "cbgpu_session_set_graphs", "cbgpu_session_rng_state",
     "cbgpu_histogram", "cbgpu_bootstrap_weights", "cbgpu_nccl_unique_id", "cbgpu_version",
     "cbgpu_session_mark", "cbgpu_session_elapsed_ms", "cbgpu_histogram_noalloc",
+    "cbgpu_rank_feature_slice", "cbgpu_rank_select_split", "cbgpu_rank_mvs_partial",
     "cbgpu_select_borders", "cbgpu_apply_oblivious",
     "cbgpu_multi_begin_raw", "cbgpu_multi_begin_cat_raw", "cbgpu_multi_grow_tree", "cbgpu_multi_approx", "cbgpu_multi_end",
     "cbgpu_rank_begin_raw",
@@ -90,6 +91,9 @@ def load(path: str = LIB_PATH):
         "cbgpu_histogram": ([vp, i64, i32, i32, vp, vp, vp, i32, vp], C.c_int),
         "cbgpu_bootstrap_weights": ([i32, i64, i64, u64, vp, f32, f32, vp, f64, vp], C.c_int),
         "cbgpu_histogram_noalloc": ([vp, i64, i32, i32, i32, vp, vp, vp, vp], C.c_int),
+        "cbgpu_rank_feature_slice": ([i32, i32, i32, vp, vp], C.c_int),
+        "cbgpu_rank_select_split": ([i32, i32, i32, vp, vp, vp, vp, vp, vp], C.c_int),
+        "cbgpu_rank_mvs_partial": ([i32, i64, vp, f64, vp, vp, f64, vp], C.c_int),
         "cbgpu_select_borders": ([vp, i64, i32, i32, i32, i32, i32, vp, vp], C.c_int),
         "cbgpu_apply_oblivious": ([vp, i64, i32, vp, vp, vp, i32, vp, vp, f64, vp, i32, vp], C.c_int),
         "cbgpu_multi_begin_raw": ([C.POINTER(BeginArgs), i32, vp, vp, vp, C.POINTER(vp)], C.c_int),

@@ -12,6 +12,9 @@
 #include <algorithm>
 #include <cfloat>
 #include <cstdio>
+#include <map>
+#include <mutex>
+#include <utility>
 
 #include "kernels.cuh"
 
@@ -20,6 +23,25 @@
 #include <cub/device/device_radix_sort.cuh>
 
 namespace cbgpu {
+
+// Raises a kernel's dynamic shared-memory limit on the current device to at
+// least `bytes`.  The attribute is per (kernel, device); the record of what
+// was set is shared by all host threads under one lock and only grows, so a
+// thread launching with fewer bytes, or on another device, never skips a
+// setting it needs.
+int ensure_dyn_smem(const void* kernel, int bytes) {
+    static std::mutex mu;
+    static std::map<std::pair<const void*, int>, int> done;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return (int)e;
+    std::lock_guard<std::mutex> lk(mu);
+    int& cur = done[{kernel, dev}];
+    if (cur >= bytes) return 0;
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess) cur = bytes;
+    return (int)e;
+}
 
 namespace {
 
@@ -57,11 +79,7 @@ __device__ __forceinline__ T block_excl_scan(T v, T* sm, T* total) {
 
 __device__ __forceinline__ double nan_to_neg_inf(double s) { return s == s ? s : -INFINITY; }
 
-// (score, index) better than (bs, bi)?  Strict > with lowest index on ties,
-// which is the CPU's first-wins strict-> scan order (tree.rs:355-366).
-__device__ __forceinline__ bool better(double s, int i, double bs, int bi) {
-    return s > bs || (s == bs && i < bi);
-}
+__device__ __forceinline__ bool better(double s, int i, double bs, int bi) { return better_split(s, i, bs, bi); }
 
 }  // namespace
 
@@ -380,14 +398,7 @@ void launch_mvs(int64_t n, int64_t row_offset, const double* wd1, const TreePara
     int64_t blocks = (n + kMvsBlock - 1) / kMvsBlock;
     if (blocks < 1) return;
     size_t smem = sizeof(double) * 2 * kMvsBlock;
-    static int attr_device = -1;  // the attribute is set per device, before any capture
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (attr_device != dev) {
-        cudaFuncSetAttribute(mvs_threshold_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)smem);
-        attr_device = dev;
-    }
+    ensure_dyn_smem((const void*)mvs_threshold_kernel, (int)smem);
     mvs_threshold_kernel<<<(unsigned)blocks, kMvsThreads, smem, st>>>(n, wd1, tp, rate, thresholds);
     mvs_weights_kernel<<<(unsigned)blocks, kMvsThreads, 0, st>>>(n, row_offset, wd1, tp, thresholds, out_sw);
 }
@@ -526,22 +537,13 @@ void launch_max_gh(int64_t n, const double* wd1, const double* weight, const flo
 __global__ void scales_kernel(TreeState* ts, int64_t n_total) {
     if (threadIdx.x != 0) return;
     for (int c = 0; c < 4; ++c) {
-        double m = __longlong_as_double((long long)ts->maxbits[c]);
-        int s = 0;
-        if (m > 0.0) {
-            int e;
-            if (c < 2) {
-                frexp(m, &e);
-                s = kPackBits - e;
-            } else {
-                frexp(m * (double)(n_total > 0 ? n_total : 1), &e);
-                s = 62 - e;
-            }
-            if (s > 1000) s = 1000;
-            if (s < -1000) s = -1000;
-        }
-        ts->sc.scale[c] = ldexp(1.0, s);
-        ts->sc.inv[c] = ldexp(1.0, -s);
+        const double m = __longlong_as_double((long long)ts->maxbits[c]);
+        // score channels: max |v| * 2^s < 2^kPackBits; leaf channels: any sum
+        // over n_total rows stays below 2^62
+        const int s = c < 2 ? fixed_shift(m, kPackBits)
+                            : fixed_shift(__dmul_rn(m, (double)(n_total > 0 ? n_total : 1)), 62);
+        ts->sc.scale[c] = pow2_of(s);
+        ts->sc.inv[c] = pow2_of(-s);
     }
 }
 
@@ -551,12 +553,7 @@ void launch_scales(TreeState* ts, int64_t n_total, cudaStream_t st) {
 
 // Per row: g = wd1 * s, h = w * s (the CPU's score channels, boosting.rs:7700-7732),
 // rounded once to fixed point and split into the (lo, hi) parts the histogram
-// accumulates: {g_lo, g_hi, h_lo, h_hi}.
-__device__ __forceinline__ void split_fixed(double v, double scale, uint32_t& lo, uint32_t& hi) {
-    const long long q = __double2ll_rn(__dmul_rn(v, scale));
-    lo = (uint32_t)(q & ((1ll << kPackSplit) - 1));
-    hi = (uint32_t)(int32_t)(q >> kPackSplit);
-}
+// accumulates: {g_lo, g_hi, h_lo, h_hi} (pack_gh).
 
 __global__ void __launch_bounds__(256) pack_stats_kernel(int64_t n, const double* __restrict__ wd1,
                                                          const double* __restrict__ weight, int s_mode,
@@ -564,15 +561,12 @@ __global__ void __launch_bounds__(256) pack_stats_kernel(int64_t n, const double
                                                          const double* __restrict__ sw64,
                                                          const TreeState* __restrict__ ts,
                                                          uint4* __restrict__ qstats) {
-    const double sg = ts->sc.scale[0], sh = ts->sc.scale[1];
+    const Pow2 sg = ts->sc.scale[0], sh = ts->sc.scale[1];
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
          i += (int64_t)gridDim.x * blockDim.x) {
         const double w = weight ? weight[i] : 1.0;
         const double s = sample_of(s_mode, sw32, sw64, i);
-        uint4 o;
-        split_fixed(__dmul_rn(wd1[i], s), sg, o.x, o.y);
-        split_fixed(__dmul_rn(w, s), sh, o.z, o.w);
-        qstats[i] = o;
+        qstats[i] = pack_gh(__dmul_rn(wd1[i], s), __dmul_rn(w, s), sg, sh);
     }
 }
 
@@ -878,15 +872,7 @@ template <bool kGather, int kFpl, int kWarps, int kStages>
 static void launch_hist_variant(unsigned gy, cudaStream_t st, const uint8_t* bins_rm, int32_t F_pad, int32_t F,
                                 int32_t B, const uint4* qstats, const uint32_t* perm, const HistChunk* chunks,
                                 const uint32_t* n_chunks, ull* built, int64_t feat_stride, int64_t slot_stride) {
-    static int attr_device = -1, attr_bins = -1;
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (attr_device != dev || attr_bins != B) {
-        cudaFuncSetAttribute(hist_kernel<kGather, kFpl, kWarps, kStages>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)hist_smem_bytes(B));
-        attr_device = dev;
-        attr_bins = B;
-    }
+    ensure_dyn_smem((const void*)hist_kernel<kGather, kFpl, kWarps, kStages>, (int)hist_smem_bytes(B));
     const dim3 grid((unsigned)hist_n_tiles(F, kFpl), gy);
     hist_kernel<kGather, kFpl, kWarps, kStages><<<grid, kWarps * 32, hist_smem_bytes(B), st>>>(
         bins_rm, F_pad, F, B, qstats, perm, chunks, n_chunks, built, feat_stride, slot_stride);
@@ -1066,7 +1052,7 @@ __global__ void __launch_bounds__(kScoreWarps * 32) score_kernel(int level, int3
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int b = g * 32 + lane;
     const bool in = b < nb;
-    const double ig = ts->sc.inv[0], ih = ts->sc.inv[1];
+    const Pow2 ig = ts->sc.inv[0], ih = ts->sc.inv[1];
     double num = 0.0, den = 1e-100;
     if (g * 32 < nb) {
         for (int c0 = 0; c0 < 2 * Q; c0 += kScorePiece) {
@@ -1096,8 +1082,8 @@ __global__ void __launch_bounds__(kScoreWarps * 32) score_kernel(int level, int3
                         pg = (long long)tot[k].x - pg;
                         ph = (long long)tot[k].y - ph;
                     }
-                    const double swd = __dmul_rn((double)pg, ig);
-                    const double sw = __dmul_rn((double)ph, ih);
+                    const double swd = from_fixed(pg, ig);
+                    const double sw = from_fixed(ph, ih);
                     if (score_fn <= 1) {  // Cosine / L2
                         const double avg = sw > 0.0 ? __ddiv_rn(swd, __dadd_rn(sw, l2)) : 0.0;
                         s_num[cc][lane] = __dmul_rn(avg, swd);
@@ -1220,21 +1206,15 @@ __global__ void select_split_kernel(int level, int world, int stride, const ull*
                                     TreeState* ts, uint8_t* __restrict__ small_side) {
     __shared__ int s_r;
     if (threadIdx.x == 0) {
-        double fb = -INFINITY;
-        int fk = 0x7fffffff, fr = -1;
-        for (int r = 0; r < world; ++r) {
-            const double sc = __longlong_as_double((long long)all_best[(size_t)r * stride]);
-            const int key = (int)(uint32_t)all_best[(size_t)r * stride + 1];
-            if (key == 0x7fffffff) continue;
-            if (better(sc, key, fb, fk)) { fb = sc; fk = key; fr = r; }
-        }
+        double fb;
+        int fk;
+        const int fr = pick_split(all_best, world, stride, &fb, &fk);
         SplitRec rec;
-        if (fk == 0x7fffffff || fb == -INFINITY) {
+        if (fr < 0) {
             rec.feature = -1;
             rec.bin = -1;
             rec.score = -INFINITY;
             atomicOr(&ts->err, kErrNoCandidate);
-            fr = -1;
         } else {
             rec.feature = fk >> 8;
             rec.bin = fk & 255;
@@ -1246,9 +1226,8 @@ __global__ void select_split_kernel(int level, int world, int stride, const ull*
     __syncthreads();
     if (!small_side) return;
     const int Q = 1 << level;
-    const ull* m = s_r >= 0 ? all_best + (size_t)s_r * stride + 2 : nullptr;
-    for (int q = threadIdx.x; q < Q; q += blockDim.x)
-        small_side[q] = m ? (m[2 * q + 1] <= m[2 * q] ? 1 : 0) : 1;
+    const ull* rec = s_r >= 0 ? all_best + (size_t)s_r * stride : nullptr;
+    for (int q = threadIdx.x; q < Q; q += blockDim.x) small_side[q] = build_true_side(rec, q);
 }
 
 void launch_select_split(int level, int world, int stride, const ull* all_best, TreeState* ts,
@@ -1639,14 +1618,14 @@ __global__ void __launch_bounds__(256) leafsum_kernel(int64_t n, const uint16_t*
         for (int k = threadIdx.x; k < 2 * L; k += blockDim.x) lsm[k] = 0ull;
         __syncthreads();
     }
-    const double sd = ts->sc.scale[2], sw = ts->sc.scale[3];
+    const Pow2 sd = ts->sc.scale[2], sw = ts->sc.scale[3];
     ull* acc = use_smem ? lsm : leaf_sums;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
          i += (int64_t)gridDim.x * blockDim.x) {
         const uint32_t q = leaf[i];
         const double w = weight ? weight[i] : 1.0;
-        atomicAdd(acc + 2 * q, (ull)__double2ll_rn(__dmul_rn(wd1[i], sd)));
-        atomicAdd(acc + 2 * q + 1, (ull)__double2ll_rn(__dmul_rn(w, sw)));
+        atomicAdd(acc + 2 * q, (ull)to_fixed(wd1[i], sd));
+        atomicAdd(acc + 2 * q + 1, (ull)to_fixed(w, sw));
     }
     if (use_smem) {
         __syncthreads();
@@ -1674,10 +1653,10 @@ __global__ void leaf_values_kernel(int depth, const ull* __restrict__ leaf_sums,
                                    const TreeState* __restrict__ ts, double* __restrict__ raw,
                                    double* __restrict__ lrv) {
     const int L = 1 << depth;
-    const double id = ts->sc.inv[2], iw = ts->sc.inv[3];
+    const Pow2 id = ts->sc.inv[2], iw = ts->sc.inv[3];
     for (int q = blockIdx.x * blockDim.x + threadIdx.x; q < L; q += gridDim.x * blockDim.x) {
-        const double sd = __dmul_rn((double)(long long)leaf_sums[2 * q], id);
-        const double sw = __dmul_rn((double)(long long)leaf_sums[2 * q + 1], iw);
+        const double sd = from_fixed((long long)leaf_sums[2 * q], id);
+        const double sw = from_fixed((long long)leaf_sums[2 * q + 1], iw);
         const double v = sw > 0.0 ? __ddiv_rn(sd, __dadd_rn(sw, l2)) : 0.0;
         raw[q] = v;
         lrv[q] = __dmul_rn(v, lr);

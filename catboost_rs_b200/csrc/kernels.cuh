@@ -1,7 +1,9 @@
 // kernels.cuh -- device kernels of the B200 oblivious-tree path and their launchers.
 #pragma once
 
+#include <cmath>
 #include <cstdint>
+#include <cstring>
 #include <utility>
 #include <cuda_runtime.h>
 
@@ -11,11 +13,58 @@ namespace cbgpu {
 
 using ull = unsigned long long;
 
+// A power of two 2^s held as two factors 2^(s/2) and 2^(s - s/2): both stay
+// normal doubles for |s| <= 2044, and (v * a) * b rounds exactly as v * 2^s
+// does whenever the result is not subnormal, so a fixed-point scale can
+// follow any finite magnitude (a channel whose largest |v| is 1e-300 still
+// gets a 2^-33-relative grid).
+struct Pow2 {
+    double a, b;
+};
+CBGPU_HD Pow2 pow2_of(int s) {
+    const int h = s / 2;
+#ifdef __CUDA_ARCH__
+    return Pow2{ldexp(1.0, h), ldexp(1.0, s - h)};
+#else
+    return Pow2{std::ldexp(1.0, h), std::ldexp(1.0, s - h)};
+#endif
+}
+// Fixed-point exponent for a channel whose largest magnitude is m: the s with
+// m * 2^s < 2^bits (0 for m == 0), clamped to +-2000 (every finite m is inside).
+CBGPU_HD int fixed_shift(double m, int bits) {
+    if (!(m > 0.0)) return 0;
+    int e = 0;
+#ifdef __CUDA_ARCH__
+    frexp(m, &e);
+#else
+    std::frexp(m, &e);
+#endif
+    int s = bits - e;
+    if (s > 2000) s = 2000;
+    if (s < -2000) s = -2000;
+    return s;
+}
+// round(v * 2^s) and q * 2^-s, both through the two factors.
+CBGPU_HD long long to_fixed(double v, Pow2 f) {
+#ifdef __CUDA_ARCH__
+    return __double2ll_rn(__dmul_rn(__dmul_rn(v, f.a), f.b));
+#else
+    return std::llrint((v * f.a) * f.b);
+#endif
+}
+CBGPU_HD double from_fixed(long long q, Pow2 inv) {
+#ifdef __CUDA_ARCH__
+    return __dmul_rn(__dmul_rn((double)q, inv.a), inv.b);
+#else
+    return ((double)q * inv.a) * inv.b;
+#endif
+}
+
 // Fixed-point scales for the four int64 accumulation channels:
 // 0 = score der (g), 1 = score weight (h), 2 = leaf der (w*der1), 3 = leaf weight (w).
 struct Scales {
-    double scale[4];
-    double inv[4];
+    Pow2 scale[4];
+    Pow2 inv[4];
 };
 
 // One histogram work item: rows [start, start+len) of the (leaf-sorted) order
@@ -67,6 +116,18 @@ constexpr int kPackBits = 33;
 constexpr int kPackSplit = 17;
 static_assert((long long)kChunkRows << kPackSplit <= (1ll << 31), "lo sums must fit 31 bits");
 static_assert((long long)kChunkRows << (kPackBits - kPackSplit) <= (1ll << 31), "hi sums must fit 31 bits");
+
+// One row's packed score channels {g_lo, g_hi, h_lo, h_hi}: g and h rounded
+// once to the channel's fixed point and split at bit kPackSplit.
+CBGPU_HD uint4 pack_gh(double g, double h, Pow2 sg, Pow2 sh) {
+    const long long qg = to_fixed(g, sg), qh = to_fixed(h, sh);
+    uint4 o;
+    o.x = (uint32_t)(qg & ((1ll << kPackSplit) - 1));
+    o.y = (uint32_t)(int32_t)(qg >> kPackSplit);
+    o.z = (uint32_t)(qh & ((1ll << kPackSplit) - 1));
+    o.w = (uint32_t)(int32_t)(qh >> kPackSplit);
+    return o;
+}
 constexpr int kPartThreads = 256;
 constexpr int kPartItems = 16;     // positions per thread in the partition kernels
 constexpr int kPartTile = kPartThreads * kPartItems;
@@ -86,6 +147,64 @@ struct SegTables {
         std::swap(mem_leaf, mem_leaf_next);
     }
 };
+
+// ---- multi-rank decisions (host and device share this code) ----------------
+//
+// Rank r of `world` derives and scores the features [f0, f0 + fs) of the
+// world * fs padded feature range (features >= F have no candidates).
+CBGPU_HD void feature_slice(int F, int world, int rank, int* f0, int* fs) {
+    *fs = (F + world - 1) / world;
+    *f0 = rank * *fs;
+}
+constexpr int kNoSplitKey = 0x7fffffff;  // a slice record without a candidate
+// (score, key) better than (bs, bk)?  Strict > with the lowest key on ties --
+// key = feature << 8 | border, so this is the CPU's first-wins strict-> scan
+// over (feature asc, border asc) (tree.rs:355-366).
+CBGPU_HD bool better_split(double s, int k, double bs, int bk) { return s > bs || (s == bs && k < bk); }
+CBGPU_HD double bits_as_double(unsigned long long b) {
+#ifdef __CUDA_ARCH__
+    return __longlong_as_double((long long)b);
+#else
+    double d;
+    memcpy(&d, &b, sizeof d);
+    return d;
+#endif
+}
+// The global split over the ranks' all-gathered slice records (`stride`
+// words each: score bits, key, then 2^level (false, true) weight sums):
+// returns the winning rank (-1 when no rank has a candidate) and its score
+// and key.  Every rank runs it on the same records, so all agree.
+CBGPU_HD int pick_split(const unsigned long long* all_best, int world, int stride, double* score, int* key) {
+    double fb = -INFINITY;
+    int fk = kNoSplitKey, fr = -1;
+    for (int r = 0; r < world; ++r) {
+        const double sc = bits_as_double(all_best[(size_t)r * stride]);
+        const int k = (int)(uint32_t)all_best[(size_t)r * stride + 1];
+        if (k == kNoSplitKey) continue;
+        if (better_split(sc, k, fb, fk)) {
+            fb = sc;
+            fk = k;
+            fr = r;
+        }
+    }
+    if (fk == kNoSplitKey || fb == -INFINITY) fr = -1;
+    *score = fb;
+    *key = fk;
+    return fr;
+}
+// The next level's build side of parent q from the winner's record: 1 (build
+// the true child) when the true child carries no more weight than the false
+// one.  Which child is built changes no result -- the sums are exact -- so
+// every rank only needs the same answer.
+CBGPU_HD uint8_t build_true_side(const unsigned long long* winner_rec, int q) {
+    if (!winner_rec) return 1;
+    const unsigned long long* m = winner_rec + 2;
+    return m[2 * q + 1] <= m[2 * q] ? 1 : 0;
+}
+
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (kernel, device)
+// and size, thread-safe; returns the cudaError_t of the setting (0 = ok).
+int ensure_dyn_smem(const void* kernel, int bytes);
 
 // ---- begin: quantization / layout ------------------------------------------
 void launch_quantize_column(const float* col, int64_t n, const double* borders, int32_t nb,

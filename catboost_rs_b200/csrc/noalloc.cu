@@ -1,14 +1,14 @@
 // noalloc.cu -- a histogram entry point that allocates no device memory.
 //
 // Some callers cannot call cudaMalloc at the moment they need a histogram:
-// code that runs while a CUDA graph is being captured (an allocation there
-// breaks or invalidates the capture), serving processes whose device memory
-// is fully reserved by their own pool allocator and who hand out only
-// pre-owned buffers, and plugins hosted in frameworks that forbid allocation
-// on their hot path.  cbgpu_histogram_noalloc serves them: the caller passes
-// device pointers for the inputs and the output, and every piece of
-// intermediate state lives in one file-scope device array below, fixed in
-// size when the library is loaded.
+// serving processes whose device memory is fully reserved by their own pool
+// allocator and who hand out only pre-owned buffers, plugins hosted in
+// frameworks that forbid allocation on their hot path, and latency-bound
+// loops that cannot afford an allocator call (or its failure) per request.
+// cbgpu_histogram_noalloc serves them: the caller passes device pointers for
+// the inputs and the output, and every piece of intermediate state lives in
+// one file-scope device array below, fixed in size when the library is
+// loaded.
 #include <cfloat>
 #include <cmath>
 #include <cstdio>
@@ -32,8 +32,13 @@ constexpr size_t kOffQstats = 0;                                              //
 constexpr size_t kOffAcc = kOffQstats + sizeof(uint4) * kNaMaxRows;           // ull [kNaMaxCells][2]
 constexpr size_t kOffChunks = kOffAcc + sizeof(ull) * 2 * kNaMaxCells;        // HistChunk [kNaMaxChunks]
 constexpr size_t kOffNChunks = kOffChunks + 256 * ((sizeof(HistChunk) * kNaMaxChunks + 255) / 256);
-constexpr size_t kOffMax = kOffNChunks + 256;                                 // ull [2] max |g|, |h| bits
+constexpr size_t kOffMax = kOffNChunks + 256;  // ull [2] max |g|, |h| bits, then the u32 error word
+constexpr size_t kOffErr = kOffMax + 2 * sizeof(unsigned long long);
 constexpr size_t kScratchBytes = kOffMax + 256;
+
+// Error word bits: the call then builds no histogram and writes NaN.
+constexpr uint32_t kNaBadBin = 1u;      // some bin >= n_bins in the first n_features columns
+constexpr uint32_t kNaNonFinite = 2u;   // some g or h is NaN or infinite
 
 // The scratch: ~5.1 MiB held by every GPU that loads the library until exit.
 // Host code must not use this name as a pointer (it is a host-side stand-in);
@@ -72,58 +77,87 @@ __global__ void na_init_kernel(int64_t n, int64_t cells) {
             ull* mx = (ull*)(g_na_scratch + kOffMax);
             mx[0] = 0ull;
             mx[1] = 0ull;
+            *(uint32_t*)(g_na_scratch + kOffErr) = 0u;
         }
     }
 }
 
+// Range check of the bins the histogram will index: the histogram kernel
+// adds into a shared-memory table of n_bins rows per feature, so a larger
+// bin would write outside it.  16-byte loads over each row's first
+// n_features bytes (the padding past them is not read by the histogram).
+__global__ void na_check_bins_kernel(int64_t n, int32_t n_features, int32_t row_stride, int32_t n_bins,
+                                     const uint8_t* __restrict__ bins) {
+    const int32_t pieces = (n_features + 15) / 16;
+    const int64_t work = n * pieces;
+    bool bad = false;
+    for (int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < work;
+         k += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = k / pieces;
+        const int32_t p = (int32_t)(k % pieces);
+        const uint4 v = *(const uint4*)(bins + r * row_stride + 16 * p);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+            bad |= 16 * p + j < n_features && ((w[j >> 2] >> (8 * (j & 3))) & 0xffu) >= (uint32_t)n_bins;
+    }
+    if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0)
+        atomicOr((uint32_t*)(g_na_scratch + kOffErr), kNaBadBin);
+}
+
+// max |g|, |h| for the fixed-point scales; NaN or infinity sets the error word
+// (fmax would drop a NaN, and an infinite maximum has no scale).
 __global__ void na_max_kernel(int64_t n, const double* __restrict__ g, const double* __restrict__ h) {
     double mg = 0.0, mh = 0.0;
+    bool bad = false;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
          i += (int64_t)gridDim.x * blockDim.x) {
-        mg = fmax(mg, fabs(g[i]));
-        mh = fmax(mh, fabs(h[i]));
+        const double a = g[i], b = h[i];
+        bad |= !isfinite(a) || !isfinite(b);
+        mg = fmax(mg, fabs(a));
+        mh = fmax(mh, fabs(b));
     }
     for (int o = 16; o > 0; o >>= 1) {
         mg = fmax(mg, __shfl_xor_sync(0xffffffffu, mg, o));
         mh = fmax(mh, __shfl_xor_sync(0xffffffffu, mh, o));
     }
+    bad = __any_sync(0xffffffffu, bad);
     ull* mx = (ull*)(g_na_scratch + kOffMax);
     if ((threadIdx.x & 31) == 0) {
         if (mg > 0.0) atomicMax(&mx[0], (ull)__double_as_longlong(mg));
         if (mh > 0.0) atomicMax(&mx[1], (ull)__double_as_longlong(mh));
+        if (bad) atomicOr((uint32_t*)(g_na_scratch + kOffErr), kNaNonFinite);
     }
 }
 
-// The session's score-channel scale rule: max |v| * 2^s < 2^kPackBits.
-__device__ __forceinline__ double na_scale(int c, bool inverse) {
+// The session's score-channel scale rule (fixed_shift, pow2_of): max |v| * 2^s < 2^kPackBits.
+__device__ __forceinline__ Pow2 na_scale(int c, bool inverse) {
     const double m = __longlong_as_double((long long)((ull*)(g_na_scratch + kOffMax))[c]);
-    int s = 0;
-    if (m > 0.0) {
-        int e;
-        frexp(m, &e);
-        s = kPackBits - e;
-    }
-    return ldexp(1.0, inverse ? -s : s);
+    const int s = fixed_shift(m, kPackBits);
+    return pow2_of(inverse ? -s : s);
 }
 
+// Packs the rows; when the checks failed, empties the work list instead so
+// the histogram kernel does nothing.
 __global__ void na_pack_kernel(int64_t n, const double* __restrict__ g, const double* __restrict__ h) {
-    const double sg = na_scale(0, false), sh = na_scale(1, false);
+    if (*(const volatile uint32_t*)(g_na_scratch + kOffErr) != 0u) {
+        if (blockIdx.x == 0 && threadIdx.x == 0) *(uint32_t*)(g_na_scratch + kOffNChunks) = 0u;
+        return;
+    }
+    const Pow2 sg = na_scale(0, false), sh = na_scale(1, false);
     uint4* qs = (uint4*)(g_na_scratch + kOffQstats);
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        const long long qg = __double2ll_rn(__dmul_rn(g[i], sg));
-        const long long qh = __double2ll_rn(__dmul_rn(h[i], sh));
-        qs[i] = make_uint4((uint32_t)(qg & ((1ll << kPackSplit) - 1)), (uint32_t)(int32_t)(qg >> kPackSplit),
-                           (uint32_t)(qh & ((1ll << kPackSplit) - 1)), (uint32_t)(int32_t)(qh >> kPackSplit));
-    }
+         i += (int64_t)gridDim.x * blockDim.x)
+        qs[i] = pack_gh(g[i], h[i], sg, sh);
 }
 
 __global__ void na_convert_kernel(int64_t cells, double* __restrict__ out) {
-    const double ig = na_scale(0, true), ih = na_scale(1, true);
+    const bool failed = *(const volatile uint32_t*)(g_na_scratch + kOffErr) != 0u;
+    const Pow2 ig = na_scale(0, true), ih = na_scale(1, true);
     const ull* acc = (const ull*)(g_na_scratch + kOffAcc);
     for (int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < 2 * cells;
          k += (int64_t)gridDim.x * blockDim.x)
-        out[k] = __dmul_rn((double)(long long)acc[k], (k & 1) ? ih : ig);
+        out[k] = failed ? __longlong_as_double(0x7ff8000000000000ll) : from_fixed((long long)acc[k], (k & 1) ? ih : ig);
 }
 
 // Device address of the scratch array on the current device (set up once per device).
@@ -180,6 +214,9 @@ int cbgpu_histogram_noalloc(const uint8_t* d_bins_row_major, int64_t n, int32_t 
     const int64_t cells = (int64_t)n_features * n_bins;
     na_init_kernel<<<grid_for(2 * cells), 256, 0, st>>>(n, cells);
     if (n > 0) {
+        if (n_bins < 256)
+            na_check_bins_kernel<<<grid_for(n * ((n_features + 15) / 16)), 256, 0, st>>>(n, n_features, row_stride,
+                                                                                      n_bins, d_bins_row_major);
         na_max_kernel<<<grid_for(n), 256, 0, st>>>(n, d_g, d_h);
         na_pack_kernel<<<grid_for(n), 256, 0, st>>>(n, d_g, d_h);
         launch_hist(d_bins_row_major, row_stride, n_features, n_bins, (const uint4*)(base + kOffQstats),
@@ -191,6 +228,19 @@ int cbgpu_histogram_noalloc(const uint8_t* d_bins_row_major, int64_t n, int32_t 
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess)
         return na_fail(CBGPU_ERR_CUDA, std::string("cbgpu_histogram_noalloc launch failed: ") + cudaGetErrorString(e));
+    // The checks' verdict: read the error word behind the work on `stream`
+    // (into host stack memory, so nothing is allocated) and wait for it.
+    uint32_t err = 0;
+    e = cudaMemcpyAsync(&err, base + kOffErr, sizeof(err), cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess)
+        return na_fail(CBGPU_ERR_CUDA, std::string("cbgpu_histogram_noalloc: ") + cudaGetErrorString(e));
+    if (err & kNaBadBin)
+        return na_fail(CBGPU_ERR_DEVICE, "cbgpu_histogram_noalloc: a bin >= n_bins = " + std::to_string(n_bins) +
+                                             " (no histogram was built; the output is NaN)");
+    if (err & kNaNonFinite)
+        return na_fail(CBGPU_ERR_DEVICE, "cbgpu_histogram_noalloc: g or h holds NaN or infinity "
+                                         "(no histogram was built; the output is NaN)");
     return CBGPU_OK;
 }
 

@@ -342,8 +342,7 @@ int alloc_session(cbgpu_session* s, const cbgpu_begin_args* a) {
     s->chunk_cap = (size_t)(n / kChunkRows) + (L / 2) + 2;
     DA(s->chunks, s->chunk_cap);
     DA(s->n_chunks, 1);
-    s->Fs = (s->F + s->world - 1) / s->world;
-    s->f0 = s->rank * s->Fs;
+    feature_slice(s->F, s->world, s->rank, &s->f0, &s->Fs);
     s->built_cells = (size_t)(L / 2 > 0 ? L / 2 : 1) * s->world * s->Fs * s->B * 2;
     s->hist_cells = (size_t)(L / 2 > 0 ? L / 2 : 1) * s->Fs * s->B * 2;
     DA(s->built, s->built_cells);
@@ -501,6 +500,29 @@ void collect_timing(cbgpu_session* s, int set) {
     }
 }
 
+}  // namespace
+
+namespace cbgpu {
+// One rank's link of the first-tree MVS lambda chain (bootstrap.rs:358-376):
+// continues the sequential f64 sum of |w * der1| (der_obj, taken through
+// sqrt(v * v) twice as the reference does) over this rank's rows, starting
+// from the previous rank's partial sum.  RMSE (loss 0) or Logloss ders at
+// approx (NULL = bias everywhere).
+double mvs_abs_der_partial(double acc, int loss, int64_t n, const double* approx, double bias, const double* target,
+                           const double* weight) {
+    for (int64_t i = 0; i < n; ++i) {
+        const double a = approx ? approx[i] : bias;
+        const double d1 = loss == 0 ? target[i] - a : target[i] - (1.0 - 1.0 / (1.0 + std::exp(a)));
+        const double v = d1 * (weight ? weight[i] : 1.0);
+        const double dobj = std::sqrt(v * v);
+        acc += std::sqrt(dobj * dobj);
+    }
+    return acc;
+}
+}  // namespace cbgpu
+
+namespace {
+
 // First-tree MVS lambda (bootstrap.rs:358-376): (sum |w*der1| / n)^2 with a
 // sequential f64 sum over all rows; the chain crosses ranks in rank order.
 int first_mvs_lambda(cbgpu_session* s, const double* approx_h, const double* target_h, double* out) {
@@ -509,6 +531,7 @@ int first_mvs_lambda(cbgpu_session* s, const double* approx_h, const double* tar
         w.resize((size_t)s->n);
         CU(cudaMemcpy(w.data(), s->weight, sizeof(double) * s->n, cudaMemcpyDeviceToHost));
     }
+    const double* wp = s->weighted ? w.data() : nullptr;
     double acc = 0.0;
     if (s->world > 1) {
         double* d;
@@ -519,13 +542,7 @@ int first_mvs_lambda(cbgpu_session* s, const double* approx_h, const double* tar
             CU(cudaMemcpyAsync(&acc, d, sizeof(double), cudaMemcpyDeviceToHost, s->st));
             CU(cudaStreamSynchronize(s->st));
         }
-        for (int64_t i = 0; i < s->n; ++i) {
-            double a = approx_h ? approx_h[i] : s->bias;
-            double d1 = s->loss == 0 ? target_h[i] - a : target_h[i] - (1.0 - 1.0 / (1.0 + std::exp(a)));
-            double v = d1 * (s->weighted ? w[(size_t)i] : 1.0);
-            double dobj = std::sqrt(v * v);
-            acc += std::sqrt(dobj * dobj);
-        }
+        acc = mvs_abs_der_partial(acc, s->loss, s->n, approx_h, s->bias, target_h, wp);
         CU(cudaMemcpyAsync(d, &acc, sizeof(double), cudaMemcpyHostToDevice, s->st));
         if (s->rank + 1 < s->world) NC(ncclSend(d, 1, ncclFloat64, s->rank + 1, s->comm, s->st));
         NC(ncclBroadcast(d, d, 1, ncclFloat64, s->world - 1, s->comm, s->st));
@@ -533,13 +550,7 @@ int first_mvs_lambda(cbgpu_session* s, const double* approx_h, const double* tar
         CU(cudaStreamSynchronize(s->st));
         cudaFree(d);
     } else {
-        for (int64_t i = 0; i < s->n; ++i) {
-            double a = approx_h ? approx_h[i] : s->bias;
-            double d1 = s->loss == 0 ? target_h[i] - a : target_h[i] - (1.0 - 1.0 / (1.0 + std::exp(a)));
-            double v = d1 * (s->weighted ? w[(size_t)i] : 1.0);
-            double dobj = std::sqrt(v * v);
-            acc += std::sqrt(dobj * dobj);
-        }
+        acc = mvs_abs_der_partial(acc, s->loss, s->n, approx_h, s->bias, target_h, wp);
     }
     double mean = s->n_total > 0 ? acc / (double)s->n_total : 0.0;
     *out = mean * mean;
@@ -1109,6 +1120,9 @@ int cbgpu_histogram(const uint8_t* bins_rm_h, int64_t n, int32_t F, int32_t B, c
             if (bins_rm_h[(size_t)i * F + f] >= B)
                 return fail(CBGPU_ERR_INVALID, "bin %d >= n_bins %d at row %lld feature %d",
                             bins_rm_h[(size_t)i * F + f], B, (long long)i, f);
+    for (int64_t i = 0; i < n; ++i)
+        if (!std::isfinite(g[i]) || !std::isfinite(h[i]))
+            return fail(CBGPU_ERR_INVALID, "non-finite g or h at row %lld", (long long)i);
     int ndev = 0;
     if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0)
         return fail(CBGPU_ERR_NO_DEVICE, "no CUDA device");
@@ -1137,7 +1151,7 @@ int cbgpu_histogram(const uint8_t* bins_rm_h, int64_t n, int32_t F, int32_t B, c
     std::vector<uint8_t> rm((size_t)std::max<int64_t>(n, 1) * F_pad, 0);
     for (int64_t i = 0; i < n; ++i) memcpy(&rm[(size_t)i * F_pad], bins_rm_h + (size_t)i * F, (size_t)F);
     // the session's scale rule for the score channels (max |v| * 2^s < 2^kPackBits)
-    double scale[2], inv[2];
+    Pow2 scale[2], inv[2];
     {
         double mx[2] = {0.0, 0.0};
         for (int64_t i = 0; i < n; ++i) {
@@ -1145,22 +1159,13 @@ int cbgpu_histogram(const uint8_t* bins_rm_h, int64_t n, int32_t F, int32_t B, c
             mx[1] = std::max(mx[1], std::fabs(h[i]));
         }
         for (int c = 0; c < 2; ++c) {
-            int sx = 0;
-            if (mx[c] > 0.0) {
-                int e;
-                std::frexp(mx[c], &e);
-                sx = kPackBits - e;
-            }
-            scale[c] = std::ldexp(1.0, sx);
-            inv[c] = std::ldexp(1.0, -sx);
+            const int sx = fixed_shift(mx[c], kPackBits);
+            scale[c] = pow2_of(sx);
+            inv[c] = pow2_of(-sx);
         }
     }
     std::vector<uint4> qs((size_t)std::max<int64_t>(n, 1));
-    for (int64_t i = 0; i < n; ++i) {
-        long long qg = std::llrint(g[i] * scale[0]), qh = std::llrint(h[i] * scale[1]);
-        qs[(size_t)i] = make_uint4((uint32_t)(qg & ((1ll << kPackSplit) - 1)), (uint32_t)(int32_t)(qg >> kPackSplit),
-                                   (uint32_t)(qh & ((1ll << kPackSplit) - 1)), (uint32_t)(int32_t)(qh >> kPackSplit));
-    }
+    for (int64_t i = 0; i < n; ++i) qs[(size_t)i] = pack_gh(g[i], h[i], scale[0], scale[1]);
     uint8_t* d_rm;
     uint4* d_qs;
     uint32_t *d_perm, *d_nch;
@@ -1185,8 +1190,45 @@ int cbgpu_histogram(const uint8_t* bins_rm_h, int64_t n, int32_t F, int32_t B, c
     CU(cudaGetLastError());
     std::vector<ull> hout(cells);
     CU(cudaMemcpy(hout.data(), d_out, sizeof(ull) * cells, cudaMemcpyDeviceToHost));
-    for (size_t k = 0; k < cells; ++k) out_hist[k] = (double)(long long)hout[k] * inv[k & 1];
+    for (size_t k = 0; k < cells; ++k) out_hist[k] = from_fixed((long long)hout[k], inv[k & 1]);
     cudaFree(d_rm); cudaFree(d_qs); cudaFree(d_perm); cudaFree(d_ch); cudaFree(d_nch); cudaFree(d_out);
+    return CBGPU_OK;
+}
+
+int cbgpu_rank_feature_slice(int32_t n_features, int32_t world, int32_t rank, int32_t* f0, int32_t* fs) {
+    if (n_features < 1 || world < 1 || rank < 0 || rank >= world || !f0 || !fs)
+        return fail(CBGPU_ERR_INVALID, "rank_feature_slice: bad arguments");
+    int a = 0, b = 0;
+    feature_slice(n_features, world, rank, &a, &b);
+    *f0 = a;
+    *fs = b;
+    return CBGPU_OK;
+}
+
+int cbgpu_rank_select_split(int32_t level, int32_t world, int32_t stride, const uint64_t* all_best,
+                            int32_t* feature, int32_t* bin, double* score, int32_t* winner_rank,
+                            uint8_t* small_side) {
+    if (level < 0 || level > 15 || world < 1 || stride < 2 + 2 * (1 << level) || !all_best || !feature || !bin ||
+        !score || !winner_rank)
+        return fail(CBGPU_ERR_INVALID, "rank_select_split: bad arguments");
+    double sc = 0.0;
+    int key = 0;
+    const int r = pick_split((const unsigned long long*)all_best, world, stride, &sc, &key);
+    *winner_rank = r;
+    *feature = r < 0 ? -1 : key >> 8;
+    *bin = r < 0 ? -1 : key & 255;
+    *score = r < 0 ? -INFINITY : sc;
+    if (small_side) {
+        const unsigned long long* rec = r >= 0 ? (const unsigned long long*)all_best + (size_t)r * stride : nullptr;
+        for (int q = 0; q < (1 << level); ++q) small_side[q] = build_true_side(rec, q);
+    }
+    return CBGPU_OK;
+}
+
+int cbgpu_rank_mvs_partial(int32_t loss, int64_t n, const double* approx, double bias, const double* target,
+                           const double* weight, double acc_in, double* acc_out) {
+    if (n < 0 || (n > 0 && !target) || !acc_out) return fail(CBGPU_ERR_INVALID, "rank_mvs_partial: bad arguments");
+    *acc_out = mvs_abs_der_partial(acc_in, loss == CBGPU_LOSS_RMSE ? 0 : 1, n, approx, bias, target, weight);
     return CBGPU_OK;
 }
 

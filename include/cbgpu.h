@@ -220,11 +220,11 @@ CBGPU_API int cbgpu_session_rng_state(cbgpu_session* s, uint64_t* out5);
 
 /* ---- building blocks (each is a standalone device computation) ------- */
 
-/* One level histogram over `n` rows: bins row-major u8 [n][n_features],
- * g/h [n] f64 score channels, leaf_of [n] (or NULL = all leaf 0).  Output
- * hist[leaf][feature][bin][2] f64 (channel 0 = sum g, 1 = sum h), computed
- * with exact int64 fixed-point accumulation (crates/cb-compute/src/
- * histogram.rs:239-294 semantics). */
+/* One level histogram over `n` rows: bins row-major u8 [n][n_features]
+ * (each < n_bins), g/h [n] finite f64 score channels, leaf_of [n] (or NULL =
+ * all leaf 0).  Output hist[leaf][feature][bin][2] f64 (channel 0 = sum g,
+ * 1 = sum h), computed with exact int64 fixed-point accumulation
+ * (crates/cb-compute/src/histogram.rs:239-294 semantics). */
 CBGPU_API int cbgpu_histogram(const uint8_t* bins_row_major, int64_t n, int32_t n_features, int32_t n_bins,
                     const double* g, const double* h, const int32_t* leaf_of, int32_t n_leaves,
                     double* out_hist);
@@ -240,24 +240,64 @@ CBGPU_API int cbgpu_bootstrap_weights(int32_t type, int64_t n, int64_t row_offse
                             const uint64_t* rng_raw4, float sample_rate, float bagging_temperature,
                             const double* der_obj, double lambda, double* out);
 
+/* ---- multi-rank decisions, run on the host ------------------------------
+ * The document-sharded session (world > 1) makes three decisions every rank
+ * must take identically; these entry points run the very code the session
+ * and its kernels use, so a host-only harness (for example gloo ranks on
+ * CPUs) can check them.  No counterpart in the reference, which trains on
+ * one device per process (crates/cb-backend/src/gpu_runtime/mod.rs:2711).
+ *
+ * cbgpu_rank_feature_slice: the features [f0, f0 + fs) of the world * fs
+ * padded range that `rank` derives and scores (features >= n_features have
+ * no candidates).
+ *
+ * cbgpu_rank_select_split: the global split of one level from the ranks'
+ * all-gathered slice records, `stride` u64 words each: the slice winner's
+ * score (f64 bits), its key (feature << 8 | border; 0x7fffffff = no
+ * candidate), then 2^level pairs of (false, true) child weight sums (u64
+ * fixed point).  The winner is the highest score, the lowest key on equal
+ * scores -- the CPU's first-wins scan over (feature, border)
+ * (crates/cb-train/src/tree.rs:355-366).  Outputs its feature / border /
+ * score and rank (-1, -1, -inf, -1 when no rank has a candidate), and, when
+ * small_side is not NULL, the next level's build side per parent [2^level]
+ * (1 = build the true child: it carries no more weight).
+ *
+ * cbgpu_rank_mvs_partial: one rank's link of the first-tree MVS lambda
+ * (crates/cb-train/src/bootstrap.rs:358-376): continues the sequential f64
+ * sum of |w * der1| over this rank's n rows from acc_in (the previous rank's
+ * result; 0 on rank 0).  loss: CBGPU_LOSS_RMSE, else the Logloss der;
+ * approx NULL = bias for every row; weight NULL = unit weights.  Chained in
+ * rank order, the last rank's sum is bit-identical to one rank's over all
+ * rows; lambda = (sum / n_total)^2. */
+CBGPU_API int cbgpu_rank_feature_slice(int32_t n_features, int32_t world, int32_t rank, int32_t* f0, int32_t* fs);
+CBGPU_API int cbgpu_rank_select_split(int32_t level, int32_t world, int32_t stride, const uint64_t* all_best,
+                                      int32_t* feature, int32_t* bin, double* score, int32_t* winner_rank,
+                                      uint8_t* small_side);
+CBGPU_API int cbgpu_rank_mvs_partial(int32_t loss, int64_t n, const double* approx, double bias,
+                                     const double* target, const double* weight, double acc_in, double* acc_out);
+
 /* Allocation-free level histogram.  No counterpart in the reference: it exists
- * for callers that cannot call cudaMalloc when they need a histogram (code
- * running under CUDA graph capture, processes whose device memory belongs to
- * their own pool allocator, hosts that forbid allocation on the hot path).
- * Inputs and output are DEVICE pointers owned by the caller: bins row-major
- * u8 [n][row_stride] (16-byte aligned; row_stride a multiple of 32 and at
- * least n_features rounded up to 32), g/h f64 [n]; out f64
- * [n_features][n_bins][2] (channel 0 = sum g, 1 = sum h), the same values
- * cbgpu_histogram returns for one leaf.  Work is enqueued on `stream`
- * (a cudaStream_t; NULL = the legacy default stream) and the call returns
- * without synchronizing.  Intermediate state lives in one fixed device array
- * of about 5.1 MiB that every GPU loading the library holds until exit; limits
- * per call: n <= 262144 rows, n_features * n_bins <= 65536, n_bins <= 256;
- * larger sizes return CBGPU_ERR_INVALID.  The first call on a device looks up
- * the array's device address (once per device), so make that first call before
- * any stream capture.  All calls share the array, which keeps the previous
- * call's contents (each call clears what must start at zero): calls that
- * overlap on the GPU, on different streams or from different threads, race. */
+ * for callers that cannot call cudaMalloc when they need a histogram
+ * (processes whose device memory belongs to their own pool allocator, hosts
+ * that forbid allocation on their hot path, latency-bound loops that cannot
+ * afford an allocator call or its failure).  Inputs and output are DEVICE
+ * pointers owned by the caller: bins row-major u8 [n][row_stride] (16-byte
+ * aligned; row_stride a multiple of 32 and at least n_features rounded up to
+ * 32), g/h f64 [n]; out f64 [n_features][n_bins][2] (channel 0 = sum g,
+ * 1 = sum h), the one-leaf histogram cbgpu_histogram computes.
+ * Preconditions checked on the device: every bin of the first n_features
+ * columns is < n_bins, and every g and h is finite; otherwise no histogram
+ * is built, the output is all NaN and the call returns CBGPU_ERR_DEVICE.
+ * Work is enqueued on `stream` (a cudaStream_t; NULL = the legacy default
+ * stream) and the call waits for it (it reads the checks' verdict back).
+ * Intermediate state lives in one fixed device array of about 5.1 MiB that
+ * every GPU loading the library holds until exit; limits per call:
+ * n <= 262144 rows, n_features * n_bins <= 65536, n_bins <= 256; larger sizes
+ * return CBGPU_ERR_INVALID.  The first call on a device looks up the array's
+ * device address (once per device), so make that first call before any
+ * stream capture.  All calls share the array, which keeps the previous call's
+ * contents (each call clears what must start at zero): calls that overlap on
+ * the GPU, on different streams or from different threads, race. */
 CBGPU_API int cbgpu_histogram_noalloc(const uint8_t* d_bins_row_major, int64_t n, int32_t n_features,
                                       int32_t row_stride, int32_t n_bins, const double* d_g,
                                       const double* d_h, double* d_out_hist, void* stream);

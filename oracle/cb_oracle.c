@@ -494,6 +494,7 @@ typedef struct {
     double std_dev;
     int32_t C;                /* one-hot cat features, candidates after the floats */
     const uint8_t* cat_bins;  /* [C][n] */
+    double* top2;             /* [depth][2] best and runner-up score per level (plain search), or NULL */
 } search_ctx;
 
 /* scan_and_score_one_hot_bins_into (histogram.rs:1160-1290): per parent the
@@ -623,6 +624,21 @@ static int search_tree(const search_ctx* c, int32_t* feat, int32_t* sbin, int32_
         free(cur);
         cur = next;
 
+        if (c->top2) {
+            /* the best and runner-up raw candidate scores (a test's near-tie bar) */
+            double best = -INFINITY, second = -INFINITY;
+            for (int32_t f = 0; f < F; ++f) {
+                const int32_t nc = f >= F0 ? NB : c->bc[f];
+                for (int32_t b = 0; b < nc; ++b) {
+                    if (f >= F0 && !present[(size_t)(f - F0) * NB + b]) continue;
+                    const double s = scores_all[(size_t)f * NB + b];
+                    if (s > best) { second = best; best = s; }
+                    else if (s > second) second = s;
+                }
+            }
+            c->top2[2 * level] = best;
+            c->top2[2 * level + 1] = second;
+        }
         int32_t best_f = -1, best_b = -1;
         if (!c->draws) {
             /* select_best: strict > over (feature asc, border asc) (tree.rs:355-366) */
@@ -699,7 +715,7 @@ static int search_tree(const search_ctx* c, int32_t* feat, int32_t* sbin, int32_
 int orc_search_tree(int64_t n, int32_t F, int32_t n_bins, int32_t depth, int32_t score_fn, const uint8_t* bins,
                     const int32_t* border_counts, const double* g, const double* h, double l2, int32_t draws,
                     orc_rng* rng, int32_t* feat, int32_t* sbin, int32_t* leaf_of, int32_t* err) {
-    search_ctx sc = {n, F, n_bins, depth, score_fn, bins, border_counts, g, h, l2, draws, rng, 0.0, 0, NULL};
+    search_ctx sc = {n, F, n_bins, depth, score_fn, bins, border_counts, g, h, l2, draws, rng, 0.0, 0, NULL, NULL};
     int e = 0;
     int taken = search_tree(&sc, feat, sbin, leaf_of, &e);
     *err = e;
@@ -797,7 +813,8 @@ int orc_train(const orc_train_args* a, orc_train_out* o) {
             std_dev = a->random_strength * dsdz * (left / (1.0 + left));
         }
         search_ctx sc = {n, F, NB, a->depth, a->score_function, a->bins_fm, a->border_counts,
-                         sg, sh, scaled_l2, draws, &rng, std_dev, a->n_cat, a->cat_bins_fm};
+                         sg, sh, scaled_l2, draws, &rng, std_dev, a->n_cat, a->cat_bins_fm,
+                         o->level_top2 ? o->level_top2 + (size_t)it * a->depth * 2 : NULL};
         int32_t* tf = o->split_feature + (size_t)it * a->depth;
         int32_t* tb = o->split_bin + (size_t)it * a->depth;
         for (int32_t l = 0; l < a->depth; ++l) { tf[l] = -1; tb[l] = -1; }

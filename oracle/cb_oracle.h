@@ -165,6 +165,8 @@ typedef struct {
     double* final_approx;    /* [n] */
     double* bias;            /* [1] starting approx */
     uint64_t* rng_calls;     /* [iterations] main-RNG call count after each tree, or NULL */
+    double* level_top2;      /* [iterations * depth * 2] best and runner-up raw candidate score per
+                                level (-inf past an early stop), or NULL */
 } orc_train_out;
 
 int orc_train(const orc_train_args* a, orc_train_out* o);

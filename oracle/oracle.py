@@ -56,7 +56,7 @@ class _TrainOut(C.Structure):
     _fields_ = [("split_feature", C.c_void_p), ("split_bin", C.c_void_p),
                 ("tree_depth", C.c_void_p), ("leaf_values", C.c_void_p),
                 ("staged", C.c_void_p), ("final_approx", C.c_void_p),
-                ("bias", C.c_void_p), ("rng_calls", C.c_void_p)]
+                ("bias", C.c_void_p), ("rng_calls", C.c_void_p), ("level_top2", C.c_void_p)]
 
 
 class _MultiArgs(C.Structure):
@@ -333,6 +333,7 @@ class OracleFit:
     final_approx: np.ndarray
     bias: float
     rng_calls: np.ndarray
+    level_top2: np.ndarray     # [iters, depth, 2] best and runner-up raw candidate score per level
 
 
 def train(bins_fm, border_counts, target, *, loss="RMSE", depth=6, iterations=10,
@@ -365,16 +366,17 @@ def train(bins_fm, border_counts, target, *, loss="RMSE", depth=6, iterations=10
     fa = np.empty(n, dtype=np.float64)
     bias = np.zeros(1, dtype=np.float64)
     calls = np.zeros(iterations, dtype=np.uint64)
+    top2 = np.full((iterations, depth, 2), -np.inf, dtype=np.float64)
     args = _TrainArgs(n, F, _p(bins), _p(bc), _p(t), _p(w), LOSS[loss], depth, iterations,
                       learning_rate, l2_leaf_reg, SCORE[score_function], BOOT[bootstrap_type],
                       subsample, bagging_temperature, random_strength, random_seed,
                       1 if boost_from_average else 0, n_threads, 0 if cb is None else cb.shape[0], _p(cb),
                       1 if exact else 0, quantile_alpha, quantile_delta)
-    out = _TrainOut(_p(sf), _p(sb), _p(td), _p(lv), _p(st), _p(fa), _p(bias), _p(calls))
+    out = _TrainOut(_p(sf), _p(sb), _p(td), _p(lv), _p(st), _p(fa), _p(bias), _p(calls), _p(top2))
     rc = lib().orc_train(C.byref(args), C.byref(out))
     if rc != 0:
         raise RuntimeError(f"orc_train failed rc={rc}")
-    return OracleFit(sf, sb, td, lv, st, fa, float(bias[0]), calls)
+    return OracleFit(sf, sb, td, lv, st, fa, float(bias[0]), calls, top2)
 
 
 @dataclass
