@@ -534,8 +534,9 @@ void launch_max_gh(int64_t n, const double* wd1, const double* weight, const flo
 // row value splits into hi = v >> 17 (|hi| <= 2^16) and lo = v & (2^17 - 1) whose
 // 32-bit sums over a kChunkRows-row work item cannot overflow; resolution is
 // 2^-33 of the largest value.  Leaf channels: max|v| * n_total * 2^s < 2^62.
-__global__ void scales_kernel(TreeState* ts, int64_t n_total) {
+__global__ void scales_kernel(TreeState* ts, int64_t n_total, int64_t n_local) {
     if (threadIdx.x != 0) return;
+    ts->hist_rows[0] = (uint32_t)n_local;  // level 0 histograms every row
     for (int c = 0; c < 4; ++c) {
         const double m = __longlong_as_double((long long)ts->maxbits[c]);
         // score channels: max |v| * 2^s < 2^kPackBits; leaf channels: any sum
@@ -547,8 +548,8 @@ __global__ void scales_kernel(TreeState* ts, int64_t n_total) {
     }
 }
 
-void launch_scales(TreeState* ts, int64_t n_total, cudaStream_t st) {
-    scales_kernel<<<1, 32, 0, st>>>(ts, n_total);
+void launch_scales(TreeState* ts, int64_t n_total, int64_t n_local, cudaStream_t st) {
+    scales_kernel<<<1, 32, 0, st>>>(ts, n_total, n_local);
 }
 
 // Per row: g = wd1 * s, h = w * s (the CPU's score channels, boosting.rs:7700-7732),
@@ -895,70 +896,26 @@ void launch_hist(const uint8_t* bins_rm, int32_t F_pad, int32_t F, int32_t B, co
     }
 }
 
-__global__ void make_chunks_kernel(int level, uint32_t* __restrict__ seg_off,
-                                   uint32_t* __restrict__ seg_cnt, uint32_t* __restrict__ mem_start,
-                                   uint32_t* __restrict__ mem_leaf,
-                                   const uint8_t* __restrict__ small_side, int64_t n0,
-                                   HistChunk* __restrict__ chunks, uint32_t cap, uint32_t* __restrict__ n_chunks,
-                                   TreeState* ts) {
-    __shared__ uint32_t s_scan[40];
-    if (level == 0) {
-        const uint32_t cr = kChunkRows;
-        uint32_t nch = (uint32_t)((n0 + cr - 1) / cr);
-        if (nch > cap) {  // cannot happen with the session's sizing; never write past the buffer
-            if (threadIdx.x == 0) atomicOr(&ts->err, kErrChunkCap);
-            nch = cap;
-        }
-        for (uint32_t k = threadIdx.x; k < nch; k += blockDim.x) {
-            uint32_t st = k * cr;
-            uint32_t ln = (uint32_t)(n0 - st < cr ? n0 - st : cr);
-            chunks[k] = HistChunk{0u, st, ln, 0u};
-        }
-        if (threadIdx.x == 0) {
-            n_chunks[0] = nch;
-            seg_off[0] = 0u;
-            seg_cnt[0] = (uint32_t)n0;
-            mem_start[0] = 0u;
-            mem_leaf[0] = 0u;
-            ts->hist_rows[0] = (uint32_t)n0;
-        }
-        return;
-    }
-    const uint32_t half = 1u << (level - 1);
-    const uint32_t per = (half + blockDim.x - 1) / blockDim.x;
-    const uint32_t p0 = threadIdx.x * per;
-    uint32_t rows = 0;
-    for (uint32_t p = p0; p < p0 + per && p < half; ++p) rows += seg_cnt[small_side[p] ? p + half : p];
-    uint32_t rows_tot;
-    (void)block_excl_scan<uint32_t>(rows, s_scan, &rows_tot);
+// The level-0 work list: rows [0, n) in kChunkRows-row items (built once per
+// session: the row count does not change).
+__global__ void level0_chunks_kernel(int64_t n, HistChunk* __restrict__ chunks, uint32_t cap,
+                                     uint32_t* __restrict__ n_chunks, uint32_t* __restrict__ err) {
     const uint32_t cr = kChunkRows;
-    uint32_t cnt = 0;
-    for (uint32_t p = p0; p < p0 + per && p < half; ++p) cnt += (seg_cnt[small_side[p] ? p + half : p] + cr - 1) / cr;
-    uint32_t tot;
-    uint32_t base = block_excl_scan<uint32_t>(cnt, s_scan, &tot);
-    for (uint32_t p = p0; p < p0 + per && p < half; ++p) {
-        uint32_t c = small_side[p] ? p + half : p;
-        uint32_t off = seg_off[c], ln = seg_cnt[c];
-        for (uint32_t st = 0; st < ln; st += cr) {
-            if (base < cap) chunks[base] = HistChunk{p, off + st, ln - st < cr ? ln - st : cr, 0u};
-            ++base;
-        }
+    uint32_t nch = (uint32_t)((n + cr - 1) / cr);
+    if (nch > cap) {  // cannot happen with the session's sizing; never write past the buffer
+        if (threadIdx.x == 0) atomicOr(err, kErrChunkCap);
+        nch = cap;
     }
-    if (threadIdx.x == 0) {
-        if (tot > cap) {  // cannot happen with the session's sizing; never write past the buffer
-            atomicOr(&ts->err, kErrChunkCap);
-            tot = cap;
-        }
-        n_chunks[0] = tot;
-        ts->hist_rows[level] = rows_tot;
+    for (uint32_t k = threadIdx.x; k < nch; k += blockDim.x) {
+        const uint32_t st = k * cr;
+        chunks[k] = HistChunk{0u, st, (uint32_t)(n - st < cr ? n - st : cr), 0u};
     }
+    if (threadIdx.x == 0) n_chunks[0] = nch;
 }
 
-void launch_make_chunks(int level, uint32_t* seg_off, uint32_t* seg_cnt, uint32_t* mem_start,
-                        uint32_t* mem_leaf, const uint8_t* small_side, int64_t n_level0,
-                        HistChunk* chunks, uint32_t cap, uint32_t* n_chunks, TreeState* ts, cudaStream_t st) {
-    make_chunks_kernel<<<1, 1024, 0, st>>>(level, seg_off, seg_cnt, mem_start, mem_leaf, small_side,
-                                           n_level0, chunks, cap, n_chunks, ts);
+void launch_level0_chunks(int64_t n, HistChunk* chunks, uint32_t cap, uint32_t* n_chunks, uint32_t* err,
+                          cudaStream_t st) {
+    level0_chunks_kernel<<<1, 1024, 0, st>>>(n, chunks, cap, n_chunks, err);
 }
 
 // ============================================================================
@@ -1236,16 +1193,7 @@ void launch_select_split(int level, int world, int stride, const ull* all_best, 
 }
 
 // ============================================================================
-// partition: stable per-segment split of the leaf-sorted row order so the next
-// level can read each child's rows contiguously.  Segments (one per leaf) are
-// contiguous position ranges; mem_start/mem_leaf list them in position order,
-// so a position's leaf is found by offset, without per-row leaf reads.
-//  P1 (count):   per tile of kPartTile positions the true-flag count, and the
-//                in-tile prefix at every segment start / end inside the tile.
-//  P2 (scan):    tile offsets, per-segment true counts, child counts and the
-//                next level's segment tables.
-//  P3 (scatter): destination of every position.
-// The last level instead writes the final leaf id of every row (natural order).
+// the chosen split of a level: the feature's column and its border
 // ============================================================================
 
 struct PartView {
@@ -1263,301 +1211,264 @@ __device__ __forceinline__ PartView part_view(const TreeState* ts, int level, co
     return v;
 }
 
-// Index of the segment (in position order) holding position j: the last k with
-// mem_start[k] <= j (empty segments share their successor's start).
-__device__ __forceinline__ int seg_of(const uint32_t* __restrict__ mem_start, int K, uint32_t j) {
-    int lo = 0, hi = K - 1;
-    while (lo < hi) {
-        int mid = (lo + hi + 1) >> 1;
-        if (mem_start[mid] <= j) lo = mid; else hi = mid - 1;
-    }
-    return lo;
-}
+// ============================================================================
+// partition by route-and-compact
+// ============================================================================
+// After split l is chosen every row's leaf id gains bit l (routing,
+// tree.rs:1005-1016), and the next level needs, for each of its 2^l parents,
+// the rows of the child it builds (the one with fewer rows -- the CPU's
+// n_true <= n_false rule, tree.rs:1111 -- or the side the ranks agreed on; the
+// sibling is derived).  Three kernels and no pass over the previous level's
+// row order:
+//  route:   leaf[i] |= (bin[f][i] > b) << l over rows in natural order (16
+//           consecutive rows per thread, 16-byte loads), with per-child row
+//           counts (block-local shared counters, one atomic per (block,
+//           child));
+//  side:    the build side per parent, the built children's segments in
+//           parent order, and a cursor per segment;
+//  compact: each block writes its built-child rows, in row order, to a range
+//           of each segment reserved with one atomic per (block, segment).
+// Rows of a segment therefore appear in block-scheduling order; the
+// histograms, exact integer sums, do not depend on it.
 
-// Walks positions [j0, j0 + cnt) of this thread, calling fn(u, j, k) with the
-// segment index k of each position.
-template <typename Fn>
-__device__ __forceinline__ void walk_segments(const uint32_t* __restrict__ mem_start, int K, uint32_t j0,
-                                              int cnt, Fn fn) {
-    int k = seg_of(mem_start, K, j0);
-    uint32_t next = k + 1 < K ? mem_start[k + 1] : 0xffffffffu;
-    for (int u = 0; u < cnt; ++u) {
-        const uint32_t j = j0 + u;
-        while (j >= next) {
-            ++k;
-            next = k + 1 < K ? mem_start[k + 1] : 0xffffffffu;
-        }
-        fn(u, j, k);
-    }
-}
+constexpr int kRouteThreads = 256;
+constexpr int kRouteRows = 16;  // consecutive rows per thread
+constexpr int kRouteTile = kRouteThreads * kRouteRows;
+constexpr int kRouteSmemChildren = 4096;  // deeper levels count with global atomics
+constexpr int kCompactSmemParents = 256;  // deeper levels reserve one slot per row
 
-// The chosen split's outcome for every row, as a bit array in natural row
-// order (bit i of word i/32 = bin > border): one coalesced pass over the
-// feature's column, so the partition kernels gather bits from a 1.25 MB array
-// (10M rows) instead of bytes from the 10 MB column.
-__global__ void __launch_bounds__(256) split_flags_kernel(int level, int64_t n,
-                                                          const uint8_t* __restrict__ bins_fm,
-                                                          int64_t n_stride,
-                                                          const TreeState* __restrict__ ts,
-                                                          uint32_t* __restrict__ flags) {
+// kNc > 0: the level has kNc <= 8 children, counted in registers and reduced
+// per warp (few distinct counters would serialize shared atomics); kNc == 0:
+// shared-memory counters (up to kRouteSmemChildren children), else global.
+template <int kNc>
+__global__ void __launch_bounds__(kRouteThreads) route_kernel(int level, int64_t n,
+                                                              const uint8_t* __restrict__ bins_fm, int64_t n_stride,
+                                                              const TreeState* __restrict__ ts,
+                                                              uint16_t* __restrict__ leaf,
+                                                              uint32_t* __restrict__ child_tot) {
+    __shared__ uint32_t s_cnt[kNc > 0 ? 8 : kRouteSmemChildren];
+    const int nc = 2 << level;
+    const bool count = child_tot != nullptr;
+    const bool smem = count && (kNc > 0 || nc <= kRouteSmemChildren);
+    if (smem) {
+        for (int k = threadIdx.x; k < (kNc > 0 ? kNc : nc); k += blockDim.x) s_cnt[k] = 0u;
+        __syncthreads();
+    }
     const PartView pv = part_view(ts, level, bins_fm, n_stride);
-    const int64_t words = (n + 31) >> 5;
-    for (int64_t w = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; w < words;
-         w += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t r0 = w << 5;
-        uint32_t bits = 0;
-        if (r0 + 32 <= n) {
-            const uint4* p = (const uint4*)(pv.col + r0);  // n_stride and r0 are multiples of 16
-            const uint4 a = __ldg(p), b = __ldg(p + 1);
-            const uint32_t v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    const int64_t r0 = (int64_t)blockIdx.x * kRouteTile + (int64_t)threadIdx.x * kRouteRows;
+    uint32_t rc[kNc > 0 ? kNc : 1];
 #pragma unroll
-            for (int k = 0; k < 32; ++k)
-                bits |= (uint32_t)((int32_t)((v[k >> 2] >> ((k & 3) * 8)) & 0xffu) > pv.bin) << k;
+    for (int v = 0; v < (kNc > 0 ? kNc : 1); ++v) rc[v] = 0u;
+    auto tally = [&](uint32_t c) {
+        if (kNc > 0) {
+#pragma unroll
+            for (int v = 0; v < (kNc > 0 ? kNc : 1); ++v) rc[v] += c == (uint32_t)v ? 1u : 0u;
+        } else if (smem) {
+            atomicAdd(&s_cnt[c], 1u);
+        } else if (count) {
+            atomicAdd(&child_tot[c], 1u);
+        }
+    };
+    if (r0 + kRouteRows <= n) {
+        const uint4 v = __ldg((const uint4*)(pv.col + r0));  // n_stride and r0 are multiples of 16
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+        uint32_t lv[kRouteRows];
+        if (level > 0) {
+            const uint4 a = ((const uint4*)(leaf + r0))[0], b = ((const uint4*)(leaf + r0))[1];
+            const uint32_t p[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+            for (int k = 0; k < kRouteRows; ++k) lv[k] = (p[k >> 1] >> ((k & 1) * 16)) & 0xffffu;
         } else {
-            for (int k = 0; r0 + k < n; ++k) bits |= (uint32_t)((int32_t)pv.col[r0 + k] > pv.bin) << k;
+#pragma unroll
+            for (int k = 0; k < kRouteRows; ++k) lv[k] = 0u;
         }
-        flags[w] = bits;
-    }
-}
-
-__device__ __forceinline__ uint32_t flag_of(const uint32_t* __restrict__ flags, uint32_t i) {
-    return (__ldg(flags + (i >> 5)) >> (i & 31)) & 1u;
-}
-
-// Positions are processed warp-striped: warp w of a tile owns kPartRounds
-// rounds of 32 consecutive positions, lane = position within the round, so
-// row-order loads are coalesced and each round's outcome is one ballot word
-// (bit lane of word j / 32 = outcome of position j).  A position's in-tile
-// true prefix is the prefix of the tile's word popcounts plus a masked popc.
-constexpr int kPartWords = kPartTile / 32;
-constexpr int kPartRounds = kPartWords / (kPartThreads / 32);
-
-// Exclusive prefix of the popcounts of the tile's kPartWords ballot words
-// (warp 0; kPartWords = 4 x 32).  Returns the tile total to every thread of warp 0.
-__device__ __forceinline__ uint32_t tile_word_prefix(const uint32_t* __restrict__ s_w, uint32_t* __restrict__ s_pre) {
-    static_assert(kPartWords == 128, "tile prefix assumes 4 words per lane");
-    const int lane = threadIdx.x & 31;
-    uint32_t c[4], t = 0;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        c[i] = (uint32_t)__popc(s_w[4 * lane + i]);
-        t += c[i];
-    }
-    const uint32_t inc = warp_incl_scan<uint32_t>(t);
-    uint32_t run = inc - t;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        s_pre[4 * lane + i] = run;
-        run += c[i];
-    }
-    return __shfl_sync(kFull, inc, 31);
-}
-
-__device__ __forceinline__ uint32_t tile_prefix_at(const uint32_t* s_w, const uint32_t* s_pre, uint32_t p) {
-    return s_pre[p >> 5] + (uint32_t)__popc(s_w[p >> 5] & ((1u << (p & 31)) - 1u));
-}
-
-__global__ void __launch_bounds__(kPartThreads) part_count_kernel(
-    int level, int64_t n, const uint32_t* __restrict__ flags_nat, const uint32_t* __restrict__ perm,
-    uint32_t* __restrict__ flags_pos, const uint32_t* __restrict__ seg_cnt,
-    const uint32_t* __restrict__ mem_start, const uint32_t* __restrict__ mem_leaf,
-    uint32_t* __restrict__ seg_start_blk, uint32_t* __restrict__ seg_start_part,
-    uint32_t* __restrict__ seg_end_blk, uint32_t* __restrict__ seg_end_part,
-    uint32_t* __restrict__ blk_true) {
-    __shared__ uint32_t s_w[kPartWords];
-    __shared__ uint32_t s_pre[kPartWords];
-    __shared__ uint32_t s_tot;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int64_t base = (int64_t)blockIdx.x * kPartTile;
-    const int64_t pw = base + (int64_t)warp * kPartRounds * 32;  // first position of this warp
-    // all row and flag loads issued before any is consumed (memory-level parallelism)
-    uint32_t row[kPartRounds], fl[kPartRounds];
-#pragma unroll
-    for (int r = 0; r < kPartRounds; ++r) {
-        const int64_t j = pw + r * 32 + lane;
-        row[r] = j < n ? (perm ? __ldg(perm + j) : (uint32_t)j) : 0xffffffffu;
-    }
-#pragma unroll
-    for (int r = 0; r < kPartRounds; ++r) fl[r] = row[r] != 0xffffffffu ? flag_of(flags_nat, row[r]) : 0u;
-#pragma unroll
-    for (int r = 0; r < kPartRounds; ++r) {
-        const uint32_t m = __ballot_sync(kFull, fl[r] != 0u);
-        if (lane == 0) {
-            s_w[warp * kPartRounds + r] = m;
-            if (pw + r * 32 < n) flags_pos[(pw >> 5) + r] = m;
+        for (int k = 0; k < kRouteRows; ++k) {
+            lv[k] |= (uint32_t)((int32_t)((w[k >> 2] >> ((k & 3) * 8)) & 0xffu) > pv.bin) << level;
+            if (count) tally(lv[k]);
+        }
+        uint4 o0, o1;
+        o0.x = lv[0] | (lv[1] << 16); o0.y = lv[2] | (lv[3] << 16);
+        o0.z = lv[4] | (lv[5] << 16); o0.w = lv[6] | (lv[7] << 16);
+        o1.x = lv[8] | (lv[9] << 16); o1.y = lv[10] | (lv[11] << 16);
+        o1.z = lv[12] | (lv[13] << 16); o1.w = lv[14] | (lv[15] << 16);
+        ((uint4*)(leaf + r0))[0] = o0;
+        ((uint4*)(leaf + r0))[1] = o1;
+    } else {
+        for (int64_t i = r0; i < n; ++i) {
+            const uint32_t c = (level > 0 ? (uint32_t)leaf[i] : 0u) |
+                               ((uint32_t)((int32_t)pv.col[i] > pv.bin) << level);
+            leaf[i] = (uint16_t)c;
+            if (count) tally(c);
         }
     }
-    __syncthreads();
-    if (warp == 0) {
-        const uint32_t tot = tile_word_prefix(s_w, s_pre);
-        if (lane == 0) s_tot = tot;
-    }
-    __syncthreads();
-    // segment starts / ends inside the tile: their exclusive / inclusive in-tile prefixes
-    const int K = 1 << level;
-    const int64_t tile_end = base + kPartTile < n ? base + kPartTile : n;
-    const int k_first = seg_of(mem_start, K, (uint32_t)base);
-    const int k_last = seg_of(mem_start, K, (uint32_t)(tile_end - 1));
-    for (int k = k_first + threadIdx.x; k <= k_last; k += blockDim.x) {
-        const uint32_t q = mem_leaf[k];
-        const uint32_t cnt = seg_cnt[q];
-        if (cnt == 0) continue;
-        const int64_t s0 = mem_start[k], e = s0 + cnt - 1;
-        if (s0 >= base && s0 < tile_end) {
-            seg_start_blk[q] = blockIdx.x;
-            seg_start_part[q] = tile_prefix_at(s_w, s_pre, (uint32_t)(s0 - base));
-        }
-        if (e >= base && e < tile_end) {
-            const uint32_t p = (uint32_t)(e - base);
-            seg_end_blk[q] = blockIdx.x;
-            seg_end_part[q] = tile_prefix_at(s_w, s_pre, p) + ((s_w[p >> 5] >> (p & 31)) & 1u);
+    if (kNc > 0 && count) {
+#pragma unroll
+        for (int v = 0; v < (kNc > 0 ? kNc : 1); ++v) {
+            uint32_t t = rc[v];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(kFull, t, o);
+            if ((threadIdx.x & 31) == 0 && t) atomicAdd(&s_cnt[v], t);
         }
     }
-    if (threadIdx.x == 0) blk_true[blockIdx.x] = s_tot;
+    if (smem) {
+        __syncthreads();
+        for (int k = threadIdx.x; k < (kNc > 0 ? kNc : nc); k += blockDim.x)
+            if (s_cnt[k]) atomicAdd(&child_tot[k], s_cnt[k]);
+    }
 }
 
-__global__ void __launch_bounds__(1024) part_scan_kernel(
-    int level, uint32_t n_tiles, uint32_t* __restrict__ blk_true,
-    const uint32_t* __restrict__ seg_off, const uint32_t* __restrict__ seg_cnt,
-    const uint32_t* __restrict__ mem_leaf,
-    const uint32_t* __restrict__ seg_start_blk, const uint32_t* __restrict__ seg_start_part,
-    const uint32_t* __restrict__ seg_end_blk, const uint32_t* __restrict__ seg_end_part,
-    uint32_t* __restrict__ t_start, uint32_t* __restrict__ f_cnt, uint32_t* __restrict__ child_cnt,
-    uint32_t* __restrict__ seg_off_next, uint32_t* __restrict__ seg_cnt_next,
-    uint32_t* __restrict__ mem_start_next, uint32_t* __restrict__ mem_leaf_next) {
+// One block: the build side of each of the Q = 2^level parents (decide: from
+// the child row counts; else the side already in small_side), the built
+// children's segments [seg_off, seg_off + cnt) in parent order with a write
+// cursor per parent, and the next level's histogram work list: each segment
+// cut into kChunkRows-row items, in parent order (cap items at most).
+__global__ void __launch_bounds__(1024) build_side_kernel(int level, int decide, const uint32_t* __restrict__ child_tot,
+                                                          uint8_t* __restrict__ small_side,
+                                                          uint32_t* __restrict__ cursor,
+                                                          HistChunk* __restrict__ chunks, uint32_t cap,
+                                                          uint32_t* __restrict__ n_chunks, TreeState* ts) {
     __shared__ uint32_t s_scan[40];
-    const uint32_t per = (n_tiles + blockDim.x - 1) / blockDim.x;
-    const uint32_t t0 = threadIdx.x * per;
-    uint32_t loc = 0;
-    for (uint32_t t = t0; t < t0 + per && t < n_tiles; ++t) loc += blk_true[t];
-    uint32_t tot;
-    uint32_t off = block_excl_scan<uint32_t>(loc, s_scan, &tot);
-    for (uint32_t t = t0; t < t0 + per && t < n_tiles; ++t) {
-        uint32_t v = blk_true[t];
-        blk_true[t] = off;
-        off += v;
-    }
-    __syncthreads();
     const uint32_t Q = 1u << level;
-    for (uint32_t q = threadIdx.x; q < Q; q += blockDim.x) {
-        const uint32_t cnt = seg_cnt[q];
-        uint32_t ts = 0, tt = 0;
-        if (cnt > 0) {
-            ts = blk_true[seg_start_blk[q]] + seg_start_part[q];
-            tt = blk_true[seg_end_blk[q]] + seg_end_part[q] - ts;
-        }
-        const uint32_t fc = cnt - tt;
-        t_start[q] = ts;
-        f_cnt[q] = fc;
-        child_cnt[q] = fc;
-        child_cnt[q + Q] = tt;
-        seg_off_next[q] = seg_off[q];
-        seg_cnt_next[q] = fc;
-        seg_off_next[q + Q] = seg_off[q] + fc;
-        seg_cnt_next[q + Q] = tt;
+    const uint32_t per = (Q + blockDim.x - 1) / blockDim.x;
+    const uint32_t q0 = threadIdx.x * per;
+    const uint32_t cr = kChunkRows;
+    uint32_t rows = 0, items = 0;
+    for (uint32_t q = q0; q < q0 + per && q < Q; ++q) {
+        if (decide) small_side[q] = child_tot[q + Q] <= child_tot[q] ? 1 : 0;
+        const uint32_t cnt = child_tot[small_side[q] ? q + Q : q];
+        rows += cnt;
+        items += (cnt + cr - 1) / cr;
     }
-    // each segment splits in place into (false child, true child)
-    for (uint32_t k = threadIdx.x; k < Q; k += blockDim.x) {
-        const uint32_t q = mem_leaf[k];
-        const uint32_t cnt = seg_cnt[q];
-        uint32_t tt = 0;
-        if (cnt > 0)
-            tt = blk_true[seg_end_blk[q]] + seg_end_part[q] - (blk_true[seg_start_blk[q]] + seg_start_part[q]);
-        mem_leaf_next[2 * k] = q;
-        mem_start_next[2 * k] = seg_off[q];
-        mem_leaf_next[2 * k + 1] = q + Q;
-        mem_start_next[2 * k + 1] = seg_off[q] + (cnt - tt);
+    uint32_t rows_tot, items_tot;
+    uint32_t off = block_excl_scan<uint32_t>(rows, s_scan, &rows_tot);
+    uint32_t item = block_excl_scan<uint32_t>(items, s_scan, &items_tot);
+    for (uint32_t q = q0; q < q0 + per && q < Q; ++q) {
+        const uint32_t cnt = child_tot[small_side[q] ? q + Q : q];
+        cursor[q] = off;
+        for (uint32_t st = 0; st < cnt; st += cr) {
+            if (item < cap) chunks[item] = HistChunk{q, off + st, cnt - st < cr ? cnt - st : cr, 0u};
+            ++item;
+        }
+        off += cnt;
+    }
+    if (threadIdx.x == 0) {
+        if (items_tot > cap) {  // cannot happen with the session's sizing; never write past the buffer
+            atomicOr(&ts->err, kErrChunkCap);
+            items_tot = cap;
+        }
+        n_chunks[0] = items_tot;
+        ts->hist_rows[level + 1] = rows_tot;
     }
 }
 
-// Destinations: a false position j of segment q goes to j - (trues before it
-// in q), a true one to seg_off[q] + f_cnt[q] + (trues before it in q); within a
-// round the false lanes and the true lanes each store to one contiguous run.
-__global__ void __launch_bounds__(kPartThreads) part_scatter_kernel(
-    int level, int64_t n, const uint32_t* __restrict__ flags_pos,
-    const uint32_t* __restrict__ perm, uint32_t* __restrict__ perm_next,
-    const uint32_t* __restrict__ seg_off, const uint32_t* __restrict__ mem_start,
-    const uint32_t* __restrict__ mem_leaf, const uint32_t* __restrict__ blk_off,
-    const uint32_t* __restrict__ t_start, const uint32_t* __restrict__ f_cnt) {
-    __shared__ uint32_t s_w[kPartWords];
-    __shared__ uint32_t s_pre[kPartWords];
+// Blocks cover the route kernel's row tiles; warp w of a block owns kRouteRows
+// rounds of 32 consecutive rows (lane = row within the round).  A row goes to
+// its parent's segment when its leaf is the built child.  Pass 1 ranks each
+// row among its warp's rows of the same parent (kQ > 0, at most 8 parents:
+// ballots; kQ == 0: per-warp shared counters, at most kCompactSmemParents),
+// the block reserves one range per parent, pass 2 writes the rows.
+template <int kQ>
+__global__ void __launch_bounds__(kRouteThreads) compact_kernel(int level, int64_t n,
+                                                                const uint16_t* __restrict__ leaf,
+                                                                const uint8_t* __restrict__ small_side,
+                                                                uint32_t* __restrict__ cursor,
+                                                                uint32_t* __restrict__ list) {
+    constexpr int kWarps = kRouteThreads / 32;
+    constexpr int kP = kQ > 0 ? kQ : kCompactSmemParents;
+    __shared__ uint32_t s_w[kWarps][kP];  // per-warp counts, then write bases
+    const uint32_t Q = 1u << level;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int64_t base = (int64_t)blockIdx.x * kPartTile;
-    const int64_t words = (n + 31) >> 5;
-    for (int k = threadIdx.x; k < kPartWords; k += blockDim.x) {
-        const int64_t w = (base >> 5) + k;
-        s_w[k] = w < words ? flags_pos[w] : 0u;
-    }
-    const int64_t pw = base + (int64_t)warp * kPartRounds * 32;
-    uint32_t row[kPartRounds];
+    const int64_t base = (int64_t)blockIdx.x * kRouteTile + (int64_t)warp * kRouteRows * 32;
+    const bool smem = Q <= (uint32_t)kP;
+    uint32_t par[kRouteRows];  // parent of this lane's row r, or ~0 when the row is not listed
 #pragma unroll
-    for (int r = 0; r < kPartRounds; ++r) {
-        const int64_t j = pw + r * 32 + lane;
-        row[r] = j < n ? (perm ? __ldg(perm + j) : (uint32_t)j) : 0u;
-    }
-    __syncthreads();
-    if (warp == 0) (void)tile_word_prefix(s_w, s_pre);
-    __syncthreads();
-    if (pw >= n) return;
-    const int K = 1 << level;
-    const uint32_t t0 = blk_off[blockIdx.x];
-    int k = seg_of(mem_start, K, (uint32_t)pw);
-    const uint32_t lt = (1u << lane) - 1u;
-#pragma unroll
-    for (int r = 0; r < kPartRounds; ++r) {
-        const int64_t j = pw + r * 32 + lane;
-        int kl = k;
-        while (kl + 1 < K && (int64_t)mem_start[kl + 1] <= j) ++kl;
-        k = __shfl_sync(kFull, kl, 31);
-        const int wi = warp * kPartRounds + r;
-        const uint32_t m = s_w[wi];
-        const uint32_t fl = (m >> lane) & 1u;
-        const uint32_t T = t0 + s_pre[wi] + (uint32_t)__popc(m & lt);
-        if (j < n) {
-            const uint32_t q = mem_leaf[kl];
-            const uint32_t rel = T - t_start[q];
-            const uint32_t dest = fl ? seg_off[q] + f_cnt[q] + rel : (uint32_t)j - rel;
-            perm_next[dest] = row[r];
+    for (int r = 0; r < kRouteRows; ++r) {
+        const int64_t i = base + r * 32 + lane;
+        par[r] = 0xffffffffu;
+        if (i < n) {
+            const uint32_t c = leaf[i];
+            const uint32_t q = c & (Q - 1u);
+            if ((c >> level) == (uint32_t)small_side[q]) par[r] = q;
         }
     }
+    if (!smem) {  // deep levels: one reserved slot per row
+#pragma unroll
+        for (int r = 0; r < kRouteRows; ++r)
+            if (par[r] != 0xffffffffu) list[atomicAdd(&cursor[par[r]], 1u)] = (uint32_t)(base + r * 32 + lane);
+        return;
+    }
+    for (uint32_t k = threadIdx.x; k < kWarps * Q; k += blockDim.x) s_w[k / Q][k % Q] = 0u;
+    __syncthreads();
+    const uint32_t lt = (1u << lane) - 1u;
+    uint32_t rank[kRouteRows];
+    if (kQ > 0) {
+        uint32_t run[kQ > 0 ? kQ : 1];
+#pragma unroll
+        for (int v = 0; v < (kQ > 0 ? kQ : 1); ++v) run[v] = 0u;
+#pragma unroll
+        for (int r = 0; r < kRouteRows; ++r) {
+            rank[r] = 0u;
+#pragma unroll
+            for (int v = 0; v < (kQ > 0 ? kQ : 1); ++v) {
+                const uint32_t m = __ballot_sync(kFull, par[r] == (uint32_t)v);
+                if (par[r] == (uint32_t)v) rank[r] = run[v] + (uint32_t)__popc(m & lt);
+                run[v] += (uint32_t)__popc(m);
+            }
+        }
+        if (lane == 0) {
+#pragma unroll
+            for (int v = 0; v < (kQ > 0 ? kQ : 1); ++v)
+                if ((uint32_t)v < Q) s_w[warp][v] = run[v];
+        }
+    } else {
+#pragma unroll
+        for (int r = 0; r < kRouteRows; ++r)
+            rank[r] = par[r] != 0xffffffffu ? atomicAdd(&s_w[warp][par[r]], 1u) : 0u;
+    }
+    __syncthreads();
+    for (uint32_t q = threadIdx.x; q < Q; q += blockDim.x) {
+        uint32_t tot = 0;
+        for (int w = 0; w < kWarps; ++w) tot += s_w[w][q];
+        uint32_t at = tot ? atomicAdd(&cursor[q], tot) : 0u;
+        for (int w = 0; w < kWarps; ++w) {
+            const uint32_t c = s_w[w][q];
+            s_w[w][q] = at;
+            at += c;
+        }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < kRouteRows; ++r)
+        if (par[r] != 0xffffffffu) list[s_w[warp][par[r]] + rank[r]] = (uint32_t)(base + r * 32 + lane);
 }
 
-void launch_partition(int level, int64_t n, const uint8_t* bins_fm, int64_t n_stride,
-                      const uint32_t* perm, uint32_t* perm_next, SegTables& sg, uint32_t* blk_true,
-                      uint32_t* flags, uint32_t* child_cnt, TreeState* ts, cudaStream_t st) {
-    const uint32_t tiles = (uint32_t)((n + kPartTile - 1) / kPartTile);
-    if (tiles == 0) return;
-    const int64_t words = (n + 31) >> 5;
-    split_flags_kernel<<<(unsigned)std::min<int64_t>((words + 255) / 256, 148 * 8), 256, 0, st>>>(
-        level, n, bins_fm, n_stride, ts, flags);
-    uint32_t* flags_pos = flags + words + 1;  // position-order outcome words
-    part_count_kernel<<<tiles, kPartThreads, 0, st>>>(level, n, flags, perm, flags_pos, sg.seg_cnt, sg.mem_start,
-                                                       sg.mem_leaf, sg.start_blk, sg.start_part, sg.end_blk,
-                                                       sg.end_part, blk_true);
-    part_scan_kernel<<<1, 1024, 0, st>>>(level, tiles, blk_true, sg.seg_off, sg.seg_cnt, sg.mem_leaf,
-                                         sg.start_blk, sg.start_part, sg.end_blk, sg.end_part, sg.t_start,
-                                         sg.f_cnt, child_cnt, sg.seg_off_next, sg.seg_cnt_next,
-                                         sg.mem_start_next, sg.mem_leaf_next);
-    part_scatter_kernel<<<tiles, kPartThreads, 0, st>>>(level, n, flags_pos, perm, perm_next, sg.seg_off,
-                                                         sg.mem_start, sg.mem_leaf, blk_true, sg.t_start,
-                                                         sg.f_cnt);
-    sg.swap();
+void launch_route(int level, int64_t n, const uint8_t* bins_fm, int64_t n_stride, uint16_t* leaf,
+                  uint32_t* child_tot, TreeState* ts, cudaStream_t st) {
+    const int64_t tiles = (n + kRouteTile - 1) / kRouteTile;
+    if (tiles <= 0) return;
+    const unsigned g = (unsigned)tiles;
+    if (child_tot && level == 0) route_kernel<2><<<g, kRouteThreads, 0, st>>>(level, n, bins_fm, n_stride, ts, leaf, child_tot);
+    else if (child_tot && level == 1) route_kernel<4><<<g, kRouteThreads, 0, st>>>(level, n, bins_fm, n_stride, ts, leaf, child_tot);
+    else if (child_tot && level == 2) route_kernel<8><<<g, kRouteThreads, 0, st>>>(level, n, bins_fm, n_stride, ts, leaf, child_tot);
+    else route_kernel<0><<<g, kRouteThreads, 0, st>>>(level, n, bins_fm, n_stride, ts, leaf, child_tot);
 }
 
-// small_side[q] = 1 when the TRUE child of q is the one to build (<= rows, as
-// the CPU's n_true <= n_false rule, tree.rs:1111).
-__global__ void small_side_kernel(int level_next, const uint32_t* __restrict__ child_cnt,
-                                  uint8_t* __restrict__ small_side) {
-    const uint32_t half = 1u << (level_next - 1);
-    for (uint32_t q = blockIdx.x * blockDim.x + threadIdx.x; q < half; q += gridDim.x * blockDim.x)
-        small_side[q] = child_cnt[q + half] <= child_cnt[q] ? 1 : 0;
+void launch_build_side(int level, bool decide, const uint32_t* child_tot, uint8_t* small_side, uint32_t* cursor,
+                       HistChunk* chunks, uint32_t cap, uint32_t* n_chunks, TreeState* ts, cudaStream_t st) {
+    build_side_kernel<<<1, 1024, 0, st>>>(level, decide ? 1 : 0, child_tot, small_side, cursor, chunks, cap,
+                                          n_chunks, ts);
 }
 
-void launch_small_side(int level_next, const uint32_t* child_cnt_global, uint8_t* small_side,
-                       cudaStream_t st) {
-    const uint32_t half = 1u << (level_next - 1);
-    unsigned blocks = (half + 255) / 256;
-    small_side_kernel<<<blocks, 256, 0, st>>>(level_next, child_cnt_global, small_side);
+void launch_compact(int level, int64_t n, const uint16_t* leaf, const uint8_t* small_side, uint32_t* cursor,
+                    uint32_t* list, cudaStream_t st) {
+    const int64_t tiles = (n + kRouteTile - 1) / kRouteTile;
+    if (tiles <= 0) return;
+    const unsigned g = (unsigned)tiles;
+    if (level == 0) compact_kernel<1><<<g, kRouteThreads, 0, st>>>(level, n, leaf, small_side, cursor, list);
+    else if (level == 1) compact_kernel<2><<<g, kRouteThreads, 0, st>>>(level, n, leaf, small_side, cursor, list);
+    else if (level == 2) compact_kernel<4><<<g, kRouteThreads, 0, st>>>(level, n, leaf, small_side, cursor, list);
+    else compact_kernel<0><<<g, kRouteThreads, 0, st>>>(level, n, leaf, small_side, cursor, list);
 }
 
 // ============================================================================
@@ -1565,47 +1476,6 @@ void launch_small_side(int level_next, const uint32_t* child_cnt_global, uint8_t
 // leaf sums (boosting.rs:2470-2517 Gradient leaves over the full w*der1 / w
 // channels) as exact int64 sums.
 // ============================================================================
-// Final leaf id of every row in natural order, straight from the tree's splits:
-// leaf = sum over levels of (bin[f_l][i] > b_l) << l.  Each thread takes 16
-// consecutive rows: one 16-byte load per level column and two 16-byte stores.
-__global__ void __launch_bounds__(256) leaf_rows_kernel(int depth, int64_t n, const uint8_t* __restrict__ bins_fm,
-                                                        int64_t n_stride, const TreeState* __restrict__ ts,
-                                                        uint16_t* __restrict__ leaf) {
-    __shared__ PartView s_pv[16];
-    if (threadIdx.x < depth) s_pv[threadIdx.x] = part_view(ts, threadIdx.x, bins_fm, n_stride);
-    __syncthreads();
-    for (int64_t g = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; g * 16 < n;
-         g += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t r0 = g * 16;
-        uint32_t lv[16];
-#pragma unroll
-        for (int k = 0; k < 16; ++k) lv[k] = 0u;
-        if (r0 + 16 <= n) {
-            for (int l = 0; l < depth; ++l) {
-                const uint4 v = __ldg((const uint4*)(s_pv[l].col + r0));  // n_stride, r0 multiples of 16
-                const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-                const int32_t bl = s_pv[l].bin;
-#pragma unroll
-                for (int k = 0; k < 16; ++k)
-                    lv[k] |= (uint32_t)((int32_t)((w[k >> 2] >> ((k & 3) * 8)) & 0xffu) > bl) << l;
-            }
-            uint4 o0, o1;
-            o0.x = lv[0] | (lv[1] << 16); o0.y = lv[2] | (lv[3] << 16);
-            o0.z = lv[4] | (lv[5] << 16); o0.w = lv[6] | (lv[7] << 16);
-            o1.x = lv[8] | (lv[9] << 16); o1.y = lv[10] | (lv[11] << 16);
-            o1.z = lv[12] | (lv[13] << 16); o1.w = lv[14] | (lv[15] << 16);
-            ((uint4*)(leaf + r0))[0] = o0;
-            ((uint4*)(leaf + r0))[1] = o1;
-        } else {
-            for (int64_t i = r0; i < n; ++i) {
-                uint32_t q = 0;
-                for (int l = 0; l < depth; ++l) q |= (uint32_t)((int32_t)s_pv[l].col[i] > s_pv[l].bin) << l;
-                leaf[i] = (uint16_t)q;
-            }
-        }
-    }
-}
-
 __global__ void __launch_bounds__(256) leafsum_kernel(int64_t n, const uint16_t* __restrict__ leaf,
                                                       const double* __restrict__ wd1,
                                                       const double* __restrict__ weight, int depth,
@@ -1634,13 +1504,9 @@ __global__ void __launch_bounds__(256) leafsum_kernel(int64_t n, const uint16_t*
     }
 }
 
-void launch_route_leafsum(int depth, int64_t n, const uint8_t* bins_fm, int64_t n_stride, uint16_t* leaf,
-                          const double* wd1, const double* weight, TreeState* ts, ull* leaf_sums,
-                          cudaStream_t st) {
+void launch_leafsum(int depth, int64_t n, const uint16_t* leaf, const double* wd1, const double* weight,
+                    TreeState* ts, ull* leaf_sums, cudaStream_t st) {
     if (n <= 0) return;
-    const int64_t groups = (n + 15) / 16;
-    leaf_rows_kernel<<<(unsigned)std::min<int64_t>((groups + 255) / 256, 148 * 8), 256, 0, st>>>(
-        depth, n, bins_fm, n_stride, ts, leaf);
     int64_t blocks = (n + 255) / 256;
     if (blocks > 148 * 4) blocks = 148 * 4;
     const size_t smem = depth <= 10 ? sizeof(ull) * 2 * (1 << depth) : 0;

@@ -128,25 +128,7 @@ CBGPU_HD uint4 pack_gh(double g, double h, Pow2 sg, Pow2 sh) {
     o.w = (uint32_t)(int32_t)(qh >> kPackSplit);
     return o;
 }
-constexpr int kPartThreads = 256;
-constexpr int kPartItems = 16;     // positions per thread in the partition kernels
-constexpr int kPartTile = kPartThreads * kPartItems;
 constexpr int kBootRun = 8;        // consecutive rows per thread in the bootstrap kernel
-
-// Leaf segments of the leaf-sorted row order: by leaf id (off, cnt) and in
-// position order (mem_start, mem_leaf); *_next are written by the partition
-// and swapped in afterwards.  start/end_* and t_start/f_cnt are P1/P2 scratch.
-struct SegTables {
-    uint32_t *seg_off, *seg_cnt, *mem_start, *mem_leaf;
-    uint32_t *seg_off_next, *seg_cnt_next, *mem_start_next, *mem_leaf_next;
-    uint32_t *start_blk, *start_part, *end_blk, *end_part, *t_start, *f_cnt;
-    void swap() {
-        std::swap(seg_off, seg_off_next);
-        std::swap(seg_cnt, seg_cnt_next);
-        std::swap(mem_start, mem_start_next);
-        std::swap(mem_leaf, mem_leaf_next);
-    }
-};
 
 // ---- multi-rank decisions (host and device share this code) ----------------
 //
@@ -230,7 +212,8 @@ void launch_der(int64_t n, int loss, double* approx, const double* target, const
                 const double* sw64, double* wd1, TreeState* ts, bool defer_gh, cudaStream_t st);
 void launch_max_gh(int64_t n, const double* wd1, const double* weight, const float* sw32, TreeState* ts,
                    cudaStream_t st);
-void launch_scales(TreeState* ts, int64_t n_total, cudaStream_t st);
+// also records this rank's level-0 row count in ts->hist_rows[0]
+void launch_scales(TreeState* ts, int64_t n_total, int64_t n_local, cudaStream_t st);
 void launch_pack_stats(int64_t n, const double* wd1, const double* weight, int s_mode, const float* sw32,
                        const double* sw64, const TreeState* ts, uint4* qstats, cudaStream_t st);
 void launch_apply(int64_t n, double* approx, const uint16_t* leaf, const double* lrv,
@@ -244,11 +227,9 @@ int hist_tiles(int32_t F, int32_t B);  // feature tiles (grid x) of the histogra
 void launch_hist(const uint8_t* bins_rm, int32_t F_pad, int32_t F, int32_t B, const uint4* qstats,
                  const uint32_t* perm, const HistChunk* chunks, const uint32_t* n_chunks, uint32_t max_chunks,
                  ull* built, int64_t feat_stride, int64_t slot_stride, cudaStream_t st);
-// level 0 also initialises the segment tables to the single all-rows segment.
-// cap = entries of `chunks`: at most n / kChunkRows + 2^(level-1) + 1 are written.
-void launch_make_chunks(int level, uint32_t* seg_off, uint32_t* seg_cnt, uint32_t* mem_start,
-                        uint32_t* mem_leaf, const uint8_t* small_side, int64_t n_level0,
-                        HistChunk* chunks, uint32_t cap, uint32_t* n_chunks, TreeState* ts, cudaStream_t st);
+// The level-0 histogram work list (all rows), built once per session.
+void launch_level0_chunks(int64_t n, HistChunk* chunks, uint32_t cap, uint32_t* n_chunks, uint32_t* err,
+                          cudaStream_t st);
 // Derive and score work on this rank's feature slice [f0, f0 + Fs) in
 // feature-major layouts (see derive_prefix_kernel).  With rank_best null the
 // winner goes to ts->split[level]; otherwise the slice winner's record goes to
@@ -262,15 +243,22 @@ void launch_score(int level, int32_t Fs, int32_t f0, int32_t F, int32_t B, const
                   TreeState* ts, ull* rank_best, cudaStream_t st);
 void launch_select_split(int level, int world, int stride, const ull* all_best, TreeState* ts,
                          uint8_t* small_side, cudaStream_t st);
-// flags: 2 * (ceil(n / 32) + 1) words (the split outcome bits, natural then position order); blk_true: ceil(n / kPartTile) + 1; child_cnt: 2^(level+1) (false counts, then true).
-void launch_partition(int level, int64_t n, const uint8_t* bins_fm, int64_t n_stride,
-                      const uint32_t* perm, uint32_t* perm_next, SegTables& sg, uint32_t* blk_true,
-                      uint32_t* flags, uint32_t* child_cnt, TreeState* ts, cudaStream_t st);
-void launch_small_side(int level_next, const uint32_t* child_cnt_global, uint8_t* small_side,
-                       cudaStream_t st);
-void launch_route_leafsum(int depth, int64_t n, const uint8_t* bins_fm, int64_t n_stride, uint16_t* leaf,
-                          const double* wd1, const double* weight, TreeState* ts, ull* leaf_sums,
-                          cudaStream_t st);
+// Routing by split `level` (leaf[i] |= (bin > border) << level; leaf[] is not
+// read at level 0), with per-child row counts added into child_tot[2 << level]
+// when child_tot is not null.
+void launch_route(int level, int64_t n, const uint8_t* bins_fm, int64_t n_stride, uint16_t* leaf,
+                  uint32_t* child_tot, TreeState* ts, cudaStream_t st);
+// The build side of each parent (decide: from child_tot; else small_side as
+// given), per-parent write cursors [2^level] of the built children's
+// segments, and the next level's histogram work list (ts->hist_rows[level + 1]).
+void launch_build_side(int level, bool decide, const uint32_t* child_tot, uint8_t* small_side, uint32_t* cursor,
+                       HistChunk* chunks, uint32_t cap, uint32_t* n_chunks, TreeState* ts, cudaStream_t st);
+// The rows of each parent's built child into list, at the cursors build_side set.
+void launch_compact(int level, int64_t n, const uint16_t* leaf, const uint8_t* small_side, uint32_t* cursor,
+                    uint32_t* list, cudaStream_t st);
+// Exact int64 sums of the unsampled w * der1 and w per final leaf.
+void launch_leafsum(int depth, int64_t n, const uint16_t* leaf, const double* wd1, const double* weight,
+                    TreeState* ts, ull* leaf_sums, cudaStream_t st);
 // Exact leaves (MAE / Quantile): keys[i] = leaf << 32 | total-order bits of
 // the f32 residual, sorted with the weights, then one block per leaf takes
 // the weighted alpha-quantile into leaf_raw / leaf_lrv.  tmp / tmp_bytes is

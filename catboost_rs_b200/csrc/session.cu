@@ -164,15 +164,14 @@ struct cbgpu_session {
     float* sw32 = nullptr;
     double* sw64 = nullptr;
     double* mvs_thr = nullptr;
-    uint16_t* leaf = nullptr;
-    uint32_t* perm[2] = {nullptr, nullptr};
-    uint32_t* seg_mem = nullptr;  // backing store of the segment tables
-    SegTables sg{};
-    uint32_t* blk_true = nullptr;
+    uint16_t* leaf = nullptr;     // every row's leaf id (routed level by level; final after the tree)
+    uint32_t* list = nullptr;     // the rows of each parent's built child, segment by segment
+    uint32_t* cursor = nullptr;   // per-parent write cursor into list
     uint32_t* child_cnt = nullptr;
-    uint32_t* flags = nullptr;    // split outcome bit per row (natural order)
     uint8_t* small_side = nullptr;
-    HistChunk* chunks = nullptr;
+    HistChunk* chunks0 = nullptr;  // level-0 work list (all rows), built at begin
+    uint32_t* n_chunks0 = nullptr;
+    HistChunk* chunks = nullptr;   // the next level's work list, built by build_side
     size_t chunk_cap = 0;
     uint32_t* n_chunks = nullptr;
     ull* built = nullptr;
@@ -322,26 +321,16 @@ int alloc_session(cbgpu_session* s, const cbgpu_begin_args* a) {
     if (s->sample_from_host) DA(s->sw64, n);
     DA(s->mvs_thr, (n + 8191) / 8192);
     DA(s->leaf, n);
-    DA(s->perm[0], n);
-    DA(s->perm[1], n);
-    {
-        const size_t Q = (size_t)1 << 16;  // up to 2^15 leaves before the last split, 2^16 after
-        DA(s->seg_mem, 14 * Q);
-        uint32_t* p = s->seg_mem;
-        uint32_t** tabs[14] = {&s->sg.seg_off, &s->sg.seg_cnt, &s->sg.mem_start, &s->sg.mem_leaf,
-                               &s->sg.seg_off_next, &s->sg.seg_cnt_next, &s->sg.mem_start_next,
-                               &s->sg.mem_leaf_next, &s->sg.start_blk, &s->sg.start_part,
-                               &s->sg.end_blk, &s->sg.end_part, &s->sg.t_start, &s->sg.f_cnt};
-        for (int k = 0; k < 14; ++k) *tabs[k] = p + (size_t)k * Q;
-    }
-    DA(s->blk_true, (n + kPartTile - 1) / kPartTile + 1);
-    DA(s->child_cnt, 1 << 17);
-    DA(s->flags, 2 * ((n + 31) / 32 + 1));  // natural-order outcome bits, then position-order words
-    DA(s->small_side, 1 << 16);
+    DA(s->list, n);
+    DA(s->cursor, 1 << 15);     // up to 2^15 parents before the last split
+    DA(s->child_cnt, 1 << 16);
+    DA(s->small_side, 1 << 15);
     // full chunks plus one partial chunk per segment
     s->chunk_cap = (size_t)(n / kChunkRows) + (L / 2) + 2;
     DA(s->chunks, s->chunk_cap);
     DA(s->n_chunks, 1);
+    DA(s->chunks0, (size_t)(n / kChunkRows) + 2);
+    DA(s->n_chunks0, 1);
     feature_slice(s->F, s->world, s->rank, &s->f0, &s->Fs);
     s->built_cells = (size_t)(L / 2 > 0 ? L / 2 : 1) * s->world * s->Fs * s->B * 2;
     s->hist_cells = (size_t)(L / 2 > 0 ? L / 2 : 1) * s->Fs * s->B * 2;
@@ -408,8 +397,8 @@ void free_session(cbgpu_session* s) {
     for (auto& g : s->graph)
         if (g) cudaGraphExecDestroy(g);
     void* ptrs[] = {s->bins_rm, s->bins_fm, s->d_border_counts, s->target, s->weight, s->approx,
-                    s->wd1, s->qstats, s->sw32, s->sw64, s->mvs_thr, s->leaf, s->perm[0], s->perm[1],
-                    s->seg_mem, s->blk_true, s->child_cnt, s->flags, s->small_side, s->chunks, s->n_chunks, s->built,
+                    s->wd1, s->qstats, s->sw32, s->sw64, s->mvs_thr, s->leaf, s->list, s->cursor,
+                    s->child_cnt, s->small_side, s->chunks0, s->n_chunks0, s->chunks, s->n_chunks, s->built,
                     s->hist[0], s->hist[1], s->feat_score, s->feat_bin, s->best_all, s->leaf_sums, s->leaf_raw,
                     s->leaf_lrv, s->ts, s->d_err, s->leaf_export, s->d_tp, s->ex_keys, s->ex_keys_sorted,
                     s->ex_w, s->ex_w_sorted, s->ex_tmp};
@@ -439,6 +428,7 @@ int finish_begin(cbgpu_session* s) {
     CU(cudaMemcpyAsync(s->d_border_counts, s->border_counts.data(), sizeof(int32_t) * s->F,
                        cudaMemcpyHostToDevice, s->st));
     if (s->n > 0) launch_transpose_fm_to_rm(s->bins_fm, s->n, s->n_stride, s->F, s->bins_rm, s->F_pad, s->st);
+    launch_level0_chunks(s->n, s->chunks0, (uint32_t)(s->n / kChunkRows) + 2, s->n_chunks0, s->d_err, s->st);
     uint32_t herr = 0;
     CU(cudaMemcpyAsync(&herr, s->d_err, sizeof(uint32_t), cudaMemcpyDeviceToHost, s->st));
     CU(cudaStreamSynchronize(s->st));
@@ -598,14 +588,13 @@ int enqueue_tree(cbgpu_session* s, int set, bool prof, int boot_mode, int s_mode
         int rc = allreduce(s, maxbits, 4, ncclUint64, ncclMax);
         if (rc) return rc;
     }
-    launch_scales(s->ts, s->n_total, st);
+    launch_scales(s->ts, s->n_total, s->n, st);
     launch_pack_stats(s->n, s->wd1, s->weight, s_mode, s->sw32, s->sw64, s->ts, s->qstats, st);
     launches += 2;
     rec(1);
 
     // ---- level loop
     int cur = 0;
-    int pp = 0;  // current perm buffer
     for (int l = 0; l < D; ++l) {
         const int e = 2 + 5 * l;
         const size_t built_slots = l == 0 ? 1 : (size_t)1 << (l - 1);
@@ -615,14 +604,12 @@ int enqueue_tree(cbgpu_session* s, int set, bool prof, int boot_mode, int s_mode
         CU(cudaMemsetAsync(s->built, 0, sizeof(ull) * slice_cells * s->world, st));
         const uint32_t max_chunks =
             (uint32_t)(s->n / kChunkRows + (l == 0 ? 1 : (1u << (l - 1))) + 1);
-        launch_make_chunks(l, s->sg.seg_off, s->sg.seg_cnt, s->sg.mem_start, s->sg.mem_leaf,
-                           l ? s->small_side : nullptr, s->n, s->chunks, (uint32_t)s->chunk_cap, s->n_chunks,
-                           s->ts, st);
         rec(e);
-        launch_hist(s->bins_rm, s->F_pad, s->F, s->B, s->qstats, l == 0 ? nullptr : s->perm[pp], s->chunks,
-                    s->n_chunks, max_chunks, s->built, (int64_t)built_slots * s->B * 2, (int64_t)s->B * 2, st);
+        launch_hist(s->bins_rm, s->F_pad, s->F, s->B, s->qstats, l == 0 ? nullptr : s->list,
+                    l == 0 ? s->chunks0 : s->chunks, l == 0 ? s->n_chunks0 : s->n_chunks, max_chunks, s->built,
+                    (int64_t)built_slots * s->B * 2, (int64_t)s->B * 2, st);
         rec(e + 1);
-        launches += 2;
+        launches += 1;
         {
             int rc = reduce_scatter_u64(s, s->built, slice_cells);
             if (rc) return rc;
@@ -644,19 +631,20 @@ int enqueue_tree(cbgpu_session* s, int set, bool prof, int boot_mode, int s_mode
         }
         rec(e + 3);
         if (l + 1 < D) {
-            launch_partition(l, s->n, s->bins_fm, s->n_stride, l == 0 ? nullptr : s->perm[pp],
-                             s->perm[pp ^ 1], s->sg, s->blk_true, s->flags, s->child_cnt, s->ts, st);
-            pp ^= 1;
+            // route every row, then list the rows of each parent's built child
+            // (single GPU: the child with fewer rows; multi-rank fits chose the
+            // side in select_split from the global weights)
+            CU(cudaMemsetAsync(s->child_cnt, 0, sizeof(uint32_t) * ((size_t)2 << l), st));
+            launch_route(l, s->n, s->bins_fm, s->n_stride, s->leaf, s->child_cnt, s->ts, st);
+            launch_build_side(l, s->world == 1, s->child_cnt, s->small_side, s->cursor, s->chunks,
+                              (uint32_t)s->chunk_cap, s->n_chunks, s->ts, st);
+            launch_compact(l, s->n, s->leaf, s->small_side, s->cursor, s->list, st);
             rec(e + 4);
-            if (s->world == 1) {  // multi-rank fits chose the build side in select_split
-                launch_small_side(l + 1, s->child_cnt, s->small_side, st);
-                ++launches;
-            }
-            launches += 4;
+            launches += 3;
         } else {
             CU(cudaMemsetAsync(s->leaf_sums, 0, sizeof(ull) * 2 * L, st));
-            launch_route_leafsum(D, s->n, s->bins_fm, s->n_stride, s->leaf, s->wd1, s->weight, s->ts,
-                                 s->leaf_sums, st);
+            launch_route(l, s->n, s->bins_fm, s->n_stride, s->leaf, nullptr, s->ts, st);
+            launch_leafsum(D, s->n, s->leaf, s->wd1, s->weight, s->ts, s->leaf_sums, st);
             launches += 2;
             rec(e + 4);
             int rc = allreduce(s, s->leaf_sums, (size_t)2 * L, ncclUint64, ncclSum);
