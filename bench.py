@@ -31,11 +31,20 @@ BLOCK_ROWS = 1 << 20       # data is generated in fixed 1Mi-row blocks so any sh
 LR_SEAM = float(np.float32(0.05))
 BORDER_SAMPLE = 200_000    # fixed-seed sample the borders are selected from (cf. cb-data's 200k sample)
 FMIN = float(np.finfo(np.float32).min)
-# DRAM bytes (read + write) per histogrammed row, from an ncu capture of all
-# eight histogram launches of one config-2-shaped tree at 2M rows (the
-# profile summary hist_kernel_dram_2M.md); the roofline's `traffic` scales it
-# by the rows each launch histograms.
-HIST_DRAM_BYTES_PER_ROW = 412.3
+# DRAM bytes (read + write) per histogrammed row of the histogram kernel, from
+# an ncu capture of the eight histogram launches of one config-2-shaped tree at
+# 2M rows, kept with the profiles; the roofline's `traffic` scales it by the
+# rows each launch histograms.
+HIST_DRAM_CAPTURE = os.path.join(ROOT, "profiles", "hist_kernel_dram_2M.json")
+
+
+def hist_dram_bytes_per_row():
+    try:
+        with open(HIST_DRAM_CAPTURE) as f:
+            d = json.load(f)
+        return float(d["dram_bytes_per_hist_row"]), d["command"]
+    except Exception:
+        return None, None
 
 
 def peaks():
@@ -387,6 +396,7 @@ def main():
     hist_launches = args.steps * args.depth
     achieved = alg_bytes / (hist_ms / 1e3) / 1e9 if hist_ms > 0 else None
     peak, peak_kind = peaks()
+    dram_per_row, dram_cmd = hist_dram_bytes_per_row()
 
     # ---- end to end through the C ABI with host buffers (e2e) --------------
     e2e = None
@@ -443,10 +453,12 @@ def main():
                 "data": "synthetic (seeded, config-2 shapes and distributions)", "config": base_cfg,
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                              "frac": (achieved / peak) if achieved else None,
-                             "traffic": HIST_DRAM_BYTES_PER_ROW * rows / hist_launches,
+                             "traffic": (dram_per_row * rows / hist_launches) if dram_per_row else None,
                              "traffic_unit": "bytes per launch",
-                             "traffic_source": "ncu capture at 2M rows, 412.3 B per histogrammed row, "
-                                               "scaled by rows per launch",
+                             "traffic_source": (f"ncu dram__bytes_read.sum + dram__bytes_write.sum of the eight "
+                                                f"histogram launches of a 2M-row tree, {dram_per_row} B per "
+                                                f"histogrammed row, scaled by rows per launch: {dram_cmd}")
+                             if dram_per_row else "no capture found",
                              "limiter": "shared-memory reduction issue: 4 exact 32-bit red.shared per "
                                         "(row, feature); LSU pipe 70.6% of peak, top stall mio_throttle "
                                         "(ncu, 2M rows)",

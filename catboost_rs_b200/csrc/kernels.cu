@@ -1362,12 +1362,13 @@ __global__ void __launch_bounds__(1024) build_side_kernel(int level, int decide,
     }
 }
 
-// Blocks cover the route kernel's row tiles; warp w of a block owns kRouteRows
-// rounds of 32 consecutive rows (lane = row within the round).  A row goes to
-// its parent's segment when its leaf is the built child.  Pass 1 ranks each
-// row among its warp's rows of the same parent (kQ > 0, at most 8 parents:
-// ballots; kQ == 0: per-warp shared counters, at most kCompactSmemParents),
-// the block reserves one range per parent, pass 2 writes the rows.
+// Blocks cover the route kernel's row tiles; thread t of a block owns its 16
+// consecutive rows (one 32-byte load of their leaf ids).  A row goes to its
+// parent's segment when its leaf is the built child.  Pass 1 ranks each row
+// among its warp's rows of the same parent (kQ > 0, at most 4 parents:
+// ballots per parent; kQ == 0: per-warp shared counters, at most
+// kCompactSmemParents parents), the block reserves one range per parent, pass
+// 2 writes the rows.
 template <int kQ>
 __global__ void __launch_bounds__(kRouteThreads) compact_kernel(int level, int64_t n,
                                                                 const uint16_t* __restrict__ leaf,
@@ -1377,29 +1378,43 @@ __global__ void __launch_bounds__(kRouteThreads) compact_kernel(int level, int64
     constexpr int kWarps = kRouteThreads / 32;
     constexpr int kP = kQ > 0 ? kQ : kCompactSmemParents;
     __shared__ uint32_t s_w[kWarps][kP];  // per-warp counts, then write bases
+    __shared__ uint8_t s_side[kP];
     const uint32_t Q = 1u << level;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int64_t base = (int64_t)blockIdx.x * kRouteTile + (int64_t)warp * kRouteRows * 32;
+    const int64_t r0 = (int64_t)blockIdx.x * kRouteTile + (int64_t)threadIdx.x * kRouteRows;
     const bool smem = Q <= (uint32_t)kP;
-    uint32_t par[kRouteRows];  // parent of this lane's row r, or ~0 when the row is not listed
+    if (smem)
+        for (uint32_t q = threadIdx.x; q < Q; q += blockDim.x) s_side[q] = small_side[q];
+    uint32_t lv[kRouteRows];
+    if (r0 + kRouteRows <= n) {
+        const uint4 a = ((const uint4*)(leaf + r0))[0], b = ((const uint4*)(leaf + r0))[1];
+        const uint32_t p[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
 #pragma unroll
-    for (int r = 0; r < kRouteRows; ++r) {
-        const int64_t i = base + r * 32 + lane;
-        par[r] = 0xffffffffu;
-        if (i < n) {
-            const uint32_t c = leaf[i];
-            const uint32_t q = c & (Q - 1u);
-            if ((c >> level) == (uint32_t)small_side[q]) par[r] = q;
-        }
+        for (int k = 0; k < kRouteRows; ++k) lv[k] = (p[k >> 1] >> ((k & 1) * 16)) & 0xffffu;
+    } else {
+#pragma unroll
+        for (int k = 0; k < kRouteRows; ++k) lv[k] = r0 + k < n ? (uint32_t)leaf[r0 + k] : 0xffffffffu;
     }
     if (!smem) {  // deep levels: one reserved slot per row
 #pragma unroll
-        for (int r = 0; r < kRouteRows; ++r)
-            if (par[r] != 0xffffffffu) list[atomicAdd(&cursor[par[r]], 1u)] = (uint32_t)(base + r * 32 + lane);
+        for (int k = 0; k < kRouteRows; ++k) {
+            if (lv[k] == 0xffffffffu) continue;
+            const uint32_t q = lv[k] & (Q - 1u);
+            if ((lv[k] >> level) == (uint32_t)small_side[q]) list[atomicAdd(&cursor[q], 1u)] = (uint32_t)(r0 + k);
+        }
         return;
     }
     for (uint32_t k = threadIdx.x; k < kWarps * Q; k += blockDim.x) s_w[k / Q][k % Q] = 0u;
     __syncthreads();
+    uint32_t par[kRouteRows];  // parent of row r0 + k, or ~0 when the row is not listed
+#pragma unroll
+    for (int k = 0; k < kRouteRows; ++k) {
+        par[k] = 0xffffffffu;
+        if (lv[k] != 0xffffffffu) {
+            const uint32_t q = lv[k] & (Q - 1u);
+            if ((lv[k] >> level) == (uint32_t)s_side[q]) par[k] = q;
+        }
+    }
     const uint32_t lt = (1u << lane) - 1u;
     uint32_t rank[kRouteRows];
     if (kQ > 0) {
@@ -1407,12 +1422,12 @@ __global__ void __launch_bounds__(kRouteThreads) compact_kernel(int level, int64
 #pragma unroll
         for (int v = 0; v < (kQ > 0 ? kQ : 1); ++v) run[v] = 0u;
 #pragma unroll
-        for (int r = 0; r < kRouteRows; ++r) {
-            rank[r] = 0u;
+        for (int k = 0; k < kRouteRows; ++k) {
+            rank[k] = 0u;
 #pragma unroll
             for (int v = 0; v < (kQ > 0 ? kQ : 1); ++v) {
-                const uint32_t m = __ballot_sync(kFull, par[r] == (uint32_t)v);
-                if (par[r] == (uint32_t)v) rank[r] = run[v] + (uint32_t)__popc(m & lt);
+                const uint32_t m = __ballot_sync(kFull, par[k] == (uint32_t)v);
+                if (par[k] == (uint32_t)v) rank[k] = run[v] + (uint32_t)__popc(m & lt);
                 run[v] += (uint32_t)__popc(m);
             }
         }
@@ -1423,8 +1438,8 @@ __global__ void __launch_bounds__(kRouteThreads) compact_kernel(int level, int64
         }
     } else {
 #pragma unroll
-        for (int r = 0; r < kRouteRows; ++r)
-            rank[r] = par[r] != 0xffffffffu ? atomicAdd(&s_w[warp][par[r]], 1u) : 0u;
+        for (int k = 0; k < kRouteRows; ++k)
+            rank[k] = par[k] != 0xffffffffu ? atomicAdd(&s_w[warp][par[k]], 1u) : 0u;
     }
     __syncthreads();
     for (uint32_t q = threadIdx.x; q < Q; q += blockDim.x) {
@@ -1439,8 +1454,8 @@ __global__ void __launch_bounds__(kRouteThreads) compact_kernel(int level, int64
     }
     __syncthreads();
 #pragma unroll
-    for (int r = 0; r < kRouteRows; ++r)
-        if (par[r] != 0xffffffffu) list[s_w[warp][par[r]] + rank[r]] = (uint32_t)(base + r * 32 + lane);
+    for (int k = 0; k < kRouteRows; ++k)
+        if (par[k] != 0xffffffffu) list[s_w[warp][par[k]] + rank[k]] = (uint32_t)(r0 + k);
 }
 
 void launch_route(int level, int64_t n, const uint8_t* bins_fm, int64_t n_stride, uint16_t* leaf,
