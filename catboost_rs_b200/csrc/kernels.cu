@@ -198,26 +198,35 @@ void launch_transpose_rm_to_fm(const uint8_t* rm, int64_t n, int32_t F, int32_t 
 // Bayesian: 1000-row blocks, block b draws from from_seed(rand_seed + b)
 // advanced 10 then one gen_rand_real1 per row (bootstrap.rs:152-175).
 // Bernoulli: the main stream continues across rows: row g uses the base state
-// advanced g draws (set_sampled_control, bootstrap.rs:178-184).  Each thread
-// jumps once and steps kBootRun consecutive rows.
-__global__ void bootstrap_kernel(int mode, int64_t n, int64_t row_offset, const TreeParams* __restrict__ tp,
-                                 double rate, float temp, float* __restrict__ out) {
-    static_assert(kBootRun == 8, "a run is stored as two float4");
-    int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-    int64_t i0 = t * kBootRun;
-    if (i0 >= n) return;
-    int64_t g0 = row_offset + i0;
-    float v[kBootRun];
+// advanced g draws (set_sampled_control, bootstrap.rs:178-184).  A thread
+// jumps once and steps kBootRun consecutive rows; the Bayesian jumps (10 to
+// 1009 steps) use the session's table of jump multipliers when given.
+__device__ __forceinline__ void jump_rng(Rng64& r, uint64_t d, const ull* __restrict__ jump) {
+    if (jump) {
+        const ull p = __ldg(jump + 2 * d), c = __ldg(jump + 2 * d + 1);
+        r.x1 = r.x1 * p + r.c1 * c;
+        r.x2 = r.x2 * p + r.c2 * c;
+    } else {
+        r.advance(d);
+    }
+}
+
+// Sample weights of rows i0 .. i0 + kBootRun - 1 (global row g0 = row_offset +
+// i0); rows at or past n get 0.
+__device__ __forceinline__ void boot_run(int mode, int64_t i0, int64_t g0, int64_t n,
+                                         const TreeParams* __restrict__ tp, double rate, float temp,
+                                         const ull* __restrict__ jump, float (&v)[kBootRun]) {
     if (mode == 1) {
         const uint64_t rand_seed = tp->boot_seed;
-        Rng64 r = Rng64::from_seed(rand_seed + (uint64_t)(g0 / 1000));
-        r.advance(10 + (uint64_t)(g0 % 1000));
+        const uint64_t blk = (uint64_t)(g0 / 1000);
+        const int rem = (int)(g0 - (int64_t)blk * 1000);
+        Rng64 r = Rng64::from_seed(rand_seed + blk);
+        jump_rng(r, 10 + (uint64_t)rem, jump);
 #pragma unroll
         for (int j = 0; j < kBootRun; ++j) {
-            int64_t g = g0 + j;
-            if (j > 0 && g % 1000 == 0) {
-                r = Rng64::from_seed(rand_seed + (uint64_t)(g / 1000));
-                r.advance(10);
+            if (j > 0 && j == 1000 - rem) {  // the run crosses into the next 1000-row block
+                r = Rng64::from_seed(rand_seed + blk + 1);
+                jump_rng(r, 10, jump);
             }
             v[j] = i0 + j < n ? (float)bayesian_weight(real1(r), temp) : 0.0f;
         }
@@ -227,6 +236,29 @@ __global__ void bootstrap_kernel(int mode, int64_t n, int64_t row_offset, const 
 #pragma unroll
         for (int j = 0; j < kBootRun; ++j) v[j] = i0 + j < n && real1(r) < rate ? 1.0f : 0.0f;
     }
+}
+
+// x -> x * A^d + c * (A^(d-1) + ... + 1) for d < kJumpSteps: jump[2d] = A^d,
+// jump[2d + 1] = the sum (the multipliers lcg_advance forms, rng.rs:45-69).
+__global__ void jump_table_kernel(ull* __restrict__ jump) {
+    const int d = blockIdx.x * blockDim.x + threadIdx.x;
+    if (d >= kJumpSteps) return;
+    jump[2 * d] = lcg_advance(1, 0, (uint64_t)d);
+    jump[2 * d + 1] = lcg_advance(0, 1, (uint64_t)d);
+}
+
+void launch_jump_table(ull* jump, cudaStream_t st) {
+    jump_table_kernel<<<(kJumpSteps + 255) / 256, 256, 0, st>>>(jump);
+}
+
+__global__ void bootstrap_kernel(int mode, int64_t n, int64_t row_offset, const TreeParams* __restrict__ tp,
+                                 double rate, float temp, const ull* __restrict__ jump, float* __restrict__ out) {
+    static_assert(kBootRun == 8, "a run is stored as two float4");
+    int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    int64_t i0 = t * kBootRun;
+    if (i0 >= n) return;
+    float v[kBootRun];
+    boot_run(mode, i0, row_offset + i0, n, tp, rate, temp, jump, v);
     if (i0 + kBootRun <= n) {  // i0 is a multiple of 8 floats: 32-byte aligned
         ((float4*)(out + i0))[0] = make_float4(v[0], v[1], v[2], v[3]);
         ((float4*)(out + i0))[1] = make_float4(v[4], v[5], v[6], v[7]);
@@ -240,7 +272,7 @@ void launch_bootstrap(int mode, int64_t n, int64_t row_offset, const TreeParams*
     int64_t threads = (n + kBootRun - 1) / kBootRun;
     int64_t blocks = (threads + 255) / 256;
     if (blocks < 1) return;
-    bootstrap_kernel<<<(unsigned)blocks, 256, 0, st>>>(mode, n, row_offset, tp, rate, temp, out_sw);
+    bootstrap_kernel<<<(unsigned)blocks, 256, 0, st>>>(mode, n, row_offset, tp, rate, temp, nullptr, out_sw);
 }
 
 // ---- MVS (bootstrap.rs:186-300): per 8192-row block a threshold from the
@@ -449,62 +481,143 @@ __device__ __forceinline__ double der1_of(int loss, double a, double t, double q
     return __dsub_rn(t, p);
 }
 
-constexpr int kDerRows = 4;  // rows per thread per step, loads issued first
+// Eight consecutive doubles from p + i0 (64-byte aligned when the run is
+// full), `fill` past n.
+__device__ __forceinline__ void load_run(const double* __restrict__ p, int64_t i0, int64_t n, bool full, double fill,
+                                         double (&v)[kBootRun]) {
+    if (full) {
+#pragma unroll
+        for (int k = 0; k < kBootRun; k += 2) {
+            const double2 x = *(const double2*)(p + i0 + k);
+            v[k] = x.x;
+            v[k + 1] = x.y;
+        }
+    } else {
+#pragma unroll
+        for (int k = 0; k < kBootRun; ++k) v[k] = i0 + k < n ? p[i0 + k] : fill;
+    }
+}
 
-__global__ void __launch_bounds__(256) der_kernel(
+__device__ __forceinline__ void store_run(double* __restrict__ p, int64_t i0, int64_t n, bool full,
+                                          const double (&v)[kBootRun]) {
+    if (full) {
+#pragma unroll
+        for (int k = 0; k < kBootRun; k += 2) *(double2*)(p + i0 + k) = make_double2(v[k], v[k + 1]);
+    } else {
+#pragma unroll
+        for (int k = 0; k < kBootRun; ++k)
+            if (i0 + k < n) p[i0 + k] = v[k];
+    }
+}
+
+// Each thread takes runs of kBootRun consecutive rows.  kBoot 1 / 2 draws the
+// run's Bayesian / Bernoulli sample here (boot_run, one RNG jump per run) and
+// stores it to sw32 as the bootstrap kernel would; otherwise the sample is
+// read as s_mode says (unless deferred to MVS).  kWeight: per-row weights.
+template <bool kWeight, int kBoot>
+__global__ void __launch_bounds__(256, 2) der_kernel(
     int64_t n, int loss, double* __restrict__ approx, const double* __restrict__ target,
     const double* __restrict__ weight, const uint16_t* __restrict__ leaf,
-    const double* __restrict__ lrv_in, const TreeParams* __restrict__ tp, int s_mode, const float* __restrict__ sw32,
-    const double* __restrict__ sw64, double* __restrict__ wd1, TreeState* ts, bool defer) {
+    const double* __restrict__ lrv_in, const TreeParams* __restrict__ tp, int s_mode, float* __restrict__ sw32,
+    const double* __restrict__ sw64, double* __restrict__ wd1, TreeState* ts, bool defer,
+    int64_t row_offset, double rate, float temp, const ull* __restrict__ jump) {
+    static_assert(kBootRun == 8, "a run is one 16-byte load of leaf ids");
     const double* lrv = tp->pending ? lrv_in : nullptr;
     const double qa = tp->q_alpha, qd = tp->q_delta;
     double m[4] = {0.0, 0.0, 0.0, 0.0};
     bool bad = false;
-    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    for (int64_t i0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i0 < n; i0 += stride * kDerRows) {
-        double a[kDerRows], t[kDerRows], w[kDerRows], sv[kDerRows];
+    const int64_t runs = (n + kBootRun - 1) / kBootRun;
+    for (int64_t run = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; run < runs;
+         run += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t i0 = run * kBootRun;
+        const bool full = i0 + kBootRun <= n;
+        double a[kBootRun], t[kBootRun], w[kBootRun], sv[kBootRun];
+        load_run(approx, i0, n, full, 0.0, a);
+        if (lrv) {
+            uint32_t id[kBootRun];
+            if (full) {
+                const uint4 p = *(const uint4*)(leaf + i0);
+                const uint32_t pw[4] = {p.x, p.y, p.z, p.w};
 #pragma unroll
-        for (int k = 0; k < kDerRows; ++k) {
-            const int64_t i = i0 + k * stride;
-            a[k] = 0.0; t[k] = 0.0; w[k] = 1.0; sv[k] = 1.0;
-            if (i < n) {
-                a[k] = approx[i];
-                if (lrv) a[k] = __dadd_rn(a[k], lrv[leaf[i]]);
-                t[k] = target[i];
-                if (weight) w[k] = weight[i];
-                if (!defer) sv[k] = sample_of(s_mode, sw32, sw64, i);
+                for (int k = 0; k < kBootRun; ++k) id[k] = (pw[k >> 1] >> ((k & 1) * 16)) & 0xffffu;
+            } else {
+#pragma unroll
+                for (int k = 0; k < kBootRun; ++k) id[k] = i0 + k < n ? leaf[i0 + k] : 0u;
             }
-        }
 #pragma unroll
-        for (int k = 0; k < kDerRows; ++k) {
-            const int64_t i = i0 + k * stride;
-            if (i >= n) continue;
-            if (lrv) approx[i] = a[k];
-            const double wd = __dmul_rn(der1_of(loss, a[k], t[k], qa, qd), w[k]);
-            wd1[i] = wd;
-            m[2] = fmax(m[2], fabs(wd));
+            for (int k = 0; k < kBootRun; ++k)
+                if (i0 + k < n) a[k] = __dadd_rn(a[k], __ldg(lrv + id[k]));
+            store_run(approx, i0, n, full, a);
+        }
+        load_run(target, i0, n, full, 0.0, t);
+        if (kWeight) {
+            load_run(weight, i0, n, full, 1.0, w);
+        } else {
+#pragma unroll
+            for (int k = 0; k < kBootRun; ++k) w[k] = 1.0;
+        }
+        if (kBoot) {
+            float v[kBootRun];
+            boot_run(kBoot, i0, row_offset + i0, n, tp, rate, temp, jump, v);
+            if (full) {
+                ((float4*)(sw32 + i0))[0] = make_float4(v[0], v[1], v[2], v[3]);
+                ((float4*)(sw32 + i0))[1] = make_float4(v[4], v[5], v[6], v[7]);
+            } else {
+                for (int k = 0; i0 + k < n; ++k) sw32[i0 + k] = v[k];
+            }
+#pragma unroll
+            for (int k = 0; k < kBootRun; ++k) sv[k] = (double)v[k];
+        } else if (!defer && s_mode == 2) {
+            load_run(sw64, i0, n, full, 1.0, sv);
+        } else {
+#pragma unroll
+            for (int k = 0; k < kBootRun; ++k)
+                sv[k] = (!defer && s_mode == 1 && i0 + k < n) ? (double)sw32[i0 + k] : 1.0;
+        }
+        double wd[kBootRun];
+#pragma unroll
+        for (int k = 0; k < kBootRun; ++k) {
+            wd[k] = 0.0;
+            if (i0 + k >= n) continue;
+            wd[k] = __dmul_rn(der1_of(loss, a[k], t[k], qa, qd), w[k]);
+            m[2] = fmax(m[2], fabs(wd[k]));
             m[3] = fmax(m[3], fabs(w[k]));
-            bad |= !isfinite(wd);
+            bad |= !isfinite(wd[k]);
             if (!defer) {
-                const double g = __dmul_rn(wd, sv[k]), h = __dmul_rn(w[k], sv[k]);
+                const double g = __dmul_rn(wd[k], sv[k]), h = __dmul_rn(w[k], sv[k]);
                 m[0] = fmax(m[0], fabs(g));
                 m[1] = fmax(m[1], fabs(h));
                 bad |= !isfinite(g) || !isfinite(h);
             }
         }
+        store_run(wd1, i0, n, full, wd);
     }
     if (bad) atomicOr(&ts->err, kErrOverflow);
     block_max4(m, ts);
 }
 
 void launch_der(int64_t n, int loss, double* approx, const double* target, const double* weight,
-                const uint16_t* leaf, const double* lrv, const TreeParams* tp, int s_mode, const float* sw32,
-                const double* sw64, double* wd1, TreeState* ts, bool defer, cudaStream_t st) {
-    int64_t blocks = (n + 255) / 256;
+                const uint16_t* leaf, const double* lrv, const TreeParams* tp, int s_mode, float* sw32,
+                const double* sw64, double* wd1, TreeState* ts, bool defer, int boot_mode, int64_t row_offset,
+                double rate, float temp, const ull* jump, cudaStream_t st) {
+    const int64_t runs = (n + kBootRun - 1) / kBootRun;
+    int64_t blocks = (runs + 255) / 256;
     if (blocks > 148 * 8) blocks = 148 * 8;
     if (blocks < 1) blocks = 1;
-    der_kernel<<<(unsigned)blocks, 256, 0, st>>>(n, loss, approx, target, weight, leaf, lrv, tp, s_mode,
-                                                 sw32, sw64, wd1, ts, defer);
+#define CBGPU_DER(W, K)                                                                                        \
+    der_kernel<W, K><<<(unsigned)blocks, 256, 0, st>>>(n, loss, approx, target, weight, leaf, lrv, tp, s_mode, sw32, \
+                                                       sw64, wd1, ts, defer, row_offset, rate, temp, jump)
+    const int k = boot_mode == 1 ? 1 : (boot_mode == 2 ? 2 : 0);
+    if (weight) {
+        if (k == 1) CBGPU_DER(true, 1);
+        else if (k == 2) CBGPU_DER(true, 2);
+        else CBGPU_DER(true, 0);
+    } else {
+        if (k == 1) CBGPU_DER(false, 1);
+        else if (k == 2) CBGPU_DER(false, 2);
+        else CBGPU_DER(false, 0);
+    }
+#undef CBGPU_DER
 }
 
 // Maxima of |g| and |h| once an MVS sample exists.
@@ -927,7 +1040,9 @@ void launch_level0_chunks(int64_t n, HistChunk* chunks, uint32_t cap, uint32_t* 
 // this rank's feature slice of Fs features: built[f][slot][B][2] (slots =
 // 2^(level-1) parents, 1 at level 0), prev[f][Q/2][B][2], cur[f][Q][B][2].
 // ============================================================================
-__global__ void derive_prefix_kernel(int level, int32_t Fs, int32_t B, const ull* __restrict__ built,
+// kDeriveRounds = ceil(B / 32) rounds of 32 bins (B <= 256).
+template <int kDeriveRounds>
+__global__ void __launch_bounds__(256) derive_prefix_kernel(int level, int32_t Fs, int32_t B, const ull* __restrict__ built,
                                      const ull* __restrict__ prev, ull* __restrict__ cur,
                                      const uint8_t* __restrict__ small_side) {
     const int lane = threadIdx.x & 31;
@@ -947,22 +1062,30 @@ __global__ void derive_prefix_kernel(int level, int32_t Fs, int32_t B, const ull
     const ulonglong2* src = (const ulonglong2*)(built + ((size_t)f * slots + p) * B * 2);
     const ulonglong2* par = (level > 0) ? (const ulonglong2*)(prev + ((size_t)f * slots + p) * B * 2) : nullptr;
     ulonglong2* dst = (ulonglong2*)(cur + ((size_t)f * Q + q) * B * 2);
-    // bins b = 32k + lane: coalesced 16-byte (g, h) pairs, prefix carried across rounds
+    // bins b = 32k + lane: coalesced 16-byte (g, h) pairs, all loads issued
+    // first, then the prefix carried across rounds
+    ulonglong2 v[kDeriveRounds], pv[kDeriveRounds];
+#pragma unroll
+    for (int k = 0; k < kDeriveRounds; ++k) {
+        const int b = 32 * k + lane;
+        v[k] = make_ulonglong2(0ull, 0ull);
+        pv[k] = make_ulonglong2(0ull, 0ull);
+        if (b < B) {
+            v[k] = src[b];
+            if (!is_built) pv[k] = par[b];
+        }
+    }
     long long cg = 0, ch = 0;
-    for (int b0 = 0; b0 < B; b0 += 32) {
-        const int b = b0 + lane;
-        ulonglong2 v = make_ulonglong2(0ull, 0ull);
-        if (b < B) v = src[b];
-        const long long ig = warp_incl_scan<long long>((long long)v.x) + cg;
-        const long long ih = warp_incl_scan<long long>((long long)v.y) + ch;
+#pragma unroll
+    for (int k = 0; k < kDeriveRounds; ++k) {
+        const int b = 32 * k + lane;
+        const long long ig = warp_incl_scan<long long>((long long)v[k].x) + cg;
+        const long long ih = warp_incl_scan<long long>((long long)v[k].y) + ch;
         cg = __shfl_sync(kFull, ig, 31);
         ch = __shfl_sync(kFull, ih, 31);
         if (b < B) {
             ulonglong2 o = make_ulonglong2((ull)ig, (ull)ih);
-            if (!is_built) {
-                const ulonglong2 pv = par[b];
-                o = make_ulonglong2((ull)((long long)pv.x - ig), (ull)((long long)pv.y - ih));
-            }
+            if (!is_built) o = make_ulonglong2((ull)((long long)pv[k].x - ig), (ull)((long long)pv[k].y - ih));
             dst[b] = o;
         }
     }
@@ -973,7 +1096,19 @@ void launch_derive_prefix(int level, int32_t Fs, int32_t B, const ull* built, co
     int64_t rows = (1ll << level) * Fs;
     int64_t blocks = (rows * 32 + 255) / 256;
     if (blocks < 1) return;
-    derive_prefix_kernel<<<(unsigned)blocks, 256, 0, st>>>(level, Fs, B, built, prev, cur, small_side);
+    const unsigned g = (unsigned)blocks;
+#define CBGPU_DERIVE(K) derive_prefix_kernel<K><<<g, 256, 0, st>>>(level, Fs, B, built, prev, cur, small_side)
+    switch ((B + 31) / 32) {
+        case 1: CBGPU_DERIVE(1); break;
+        case 2: CBGPU_DERIVE(2); break;
+        case 3: CBGPU_DERIVE(3); break;
+        case 4: CBGPU_DERIVE(4); break;
+        case 5: CBGPU_DERIVE(5); break;
+        case 6: CBGPU_DERIVE(6); break;
+        case 7: CBGPU_DERIVE(7); break;
+        default: CBGPU_DERIVE(8); break;
+    }
+#undef CBGPU_DERIVE
 }
 
 // ============================================================================
@@ -983,22 +1118,25 @@ void launch_derive_prefix(int level, int32_t Fs, int32_t B, const ull* built, co
 // The per-child terms avg*swd and avg^2*sw are independent, so the 8 warps
 // compute a piece of kScorePiece children into shared memory; then warp 0 adds
 // them to each border's running sums in the CPU's canonical order (false
-// children 0..Q-1, then true), so the sums round as the CPU's do.  The last
-// block to finish reduces the per-group winners in (feature, border) order,
-// which is the CPU's first-wins strict-> scan (no spin wait).
+// children 0..Q-1, then true), so the sums round as the CPU's do.  The true
+// children's totals (bin B-1 of each leaf's prefix row) are staged once per
+// block.  The last block to finish reduces the per-group winners in (feature,
+// border) order, which is the CPU's first-wins strict-> scan (no spin wait).
 // ============================================================================
 constexpr int kScoreWarps = 8;
-constexpr int kScorePiece = 64;  // children per piece, kScorePiece / kScoreWarps per warp
+constexpr int kScorePiece = 64;      // children per piece, kScorePiece / kScoreWarps per warp
+constexpr int kScoreTotSmem = 256;   // leaves whose totals are staged in shared memory
 
-__global__ void __launch_bounds__(kScoreWarps * 32) score_kernel(int level, int32_t Fs, int32_t f0, int32_t F,
-                                                                 int32_t B, const ull* __restrict__ cur,
-                                                                 const int32_t* __restrict__ border_counts,
-                                                                 double l2, int score_fn,
-                                                                 double* __restrict__ grp_score,
-                                                                 int32_t* __restrict__ grp_bin, TreeState* ts,
-                                                                 ull* __restrict__ rank_best) {
-    __shared__ double s_num[kScorePiece][32];
-    __shared__ double s_den[kScorePiece][32];
+__global__ void __launch_bounds__(kScoreWarps * 32, 4) score_kernel(int level, int32_t Fs, int32_t f0, int32_t F,
+                                                                    int32_t B, const ull* __restrict__ cur,
+                                                                    const int32_t* __restrict__ border_counts,
+                                                                    double l2, int score_fn,
+                                                                    double* __restrict__ grp_score,
+                                                                    int32_t* __restrict__ grp_bin, TreeState* ts,
+                                                                    ull* __restrict__ rank_best,
+                                                                    uint8_t* __restrict__ small_side) {
+    __shared__ double2 s_t[kScorePiece][32];  // (num, den) terms of a piece
+    __shared__ ulonglong2 s_tot[kScoreTotSmem];
     __shared__ double s_sc[kScoreWarps];
     __shared__ int s_bi[kScoreWarps];
     __shared__ bool s_last;
@@ -1010,51 +1148,80 @@ __global__ void __launch_bounds__(kScoreWarps * 32) score_kernel(int level, int3
     const int b = g * 32 + lane;
     const bool in = b < nb;
     const Pow2 ig = ts->sc.inv[0], ih = ts->sc.inv[1];
+    const ulonglong2* rows = (const ulonglong2*)(cur + (size_t)fl * Q * B * 2);  // row q at rows + q * B
+    const bool tot_smem = Q <= kScoreTotSmem;
     double num = 0.0, den = 1e-100;
     if (g * 32 < nb) {
+        if (tot_smem) {
+            for (int q = threadIdx.x; q < Q; q += blockDim.x) s_tot[q] = rows[(size_t)q * B + B - 1];
+            __syncthreads();
+        }
         for (int c0 = 0; c0 < 2 * Q; c0 += kScorePiece) {
             const int pc = 2 * Q - c0 < kScorePiece ? 2 * Q - c0 : kScorePiece;
             constexpr int kPer = kScorePiece / kScoreWarps;
-            ulonglong2 v[kPer], tot[kPer];
+            ulonglong2 v[kPer];
 #pragma unroll
             for (int k = 0; k < kPer; ++k) {
                 const int cc = warp + k * kScoreWarps;
                 v[k] = make_ulonglong2(0ull, 0ull);
-                tot[k] = make_ulonglong2(0ull, 0ull);
                 if (cc < pc && in) {
                     const int ch = c0 + cc;  // canonical child index: side * Q + q
-                    const int side = ch >= Q, q = ch - side * Q;
-                    const ulonglong2* row = (const ulonglong2*)(cur + ((size_t)fl * Q + q) * B * 2);
-                    v[k] = row[b];
-                    if (side) tot[k] = row[B - 1];
+                    const int q = ch >= Q ? ch - Q : ch;
+                    v[k] = rows[(size_t)q * B + b];
                 }
             }
 #pragma unroll
             for (int k = 0; k < kPer; ++k) {
                 const int cc = warp + k * kScoreWarps;
                 if (cc < pc && in) {
-                    const int side = c0 + cc >= Q;
+                    const int ch = c0 + cc;
                     long long pg = (long long)v[k].x, ph = (long long)v[k].y;
-                    if (side) {
-                        pg = (long long)tot[k].x - pg;
-                        ph = (long long)tot[k].y - ph;
+                    if (ch >= Q) {
+                        const int q = ch - Q;
+                        const ulonglong2 t = tot_smem ? s_tot[q] : rows[(size_t)q * B + B - 1];
+                        pg = (long long)t.x - pg;
+                        ph = (long long)t.y - ph;
                     }
                     const double swd = from_fixed(pg, ig);
                     const double sw = from_fixed(ph, ih);
+                    double2 term;
                     if (score_fn <= 1) {  // Cosine / L2
                         const double avg = sw > 0.0 ? __ddiv_rn(swd, __dadd_rn(sw, l2)) : 0.0;
-                        s_num[cc][lane] = __dmul_rn(avg, swd);
-                        s_den[cc][lane] = __dmul_rn(__dmul_rn(avg, avg), sw);
+                        term = make_double2(__dmul_rn(avg, swd), __dmul_rn(__dmul_rn(avg, avg), sw));
                     } else {  // SolarL2 / LOOL2 / SatL2: the sum of per-leaf terms
-                        s_num[cc][lane] = gpu_score_term(score_fn, swd, sw);
+                        term = make_double2(gpu_score_term(score_fn, swd, sw), 0.0);
                     }
+                    s_t[cc][lane] = term;
                 }
             }
             __syncthreads();
             if (warp == 0 && in) {
-                for (int cc = 0; cc < pc; ++cc) {
-                    num = __dadd_rn(num, s_num[cc][lane]);
-                    if (score_fn == 0) den = __dadd_rn(den, s_den[cc][lane]);
+                int cc = 0;
+                if (score_fn == 0) {
+                    for (; cc + 8 <= pc; cc += 8) {
+                        double2 t[8];
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) t[k] = s_t[cc + k][lane];
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) {
+                            num = __dadd_rn(num, t[k].x);
+                            den = __dadd_rn(den, t[k].y);
+                        }
+                    }
+                    for (; cc < pc; ++cc) {
+                        const double2 t = s_t[cc][lane];
+                        num = __dadd_rn(num, t.x);
+                        den = __dadd_rn(den, t.y);
+                    }
+                } else {
+                    for (; cc + 8 <= pc; cc += 8) {
+                        double t[8];
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) t[k] = s_t[cc + k][lane].x;
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) num = __dadd_rn(num, t[k]);
+                    }
+                    for (; cc < pc; ++cc) num = __dadd_rn(num, s_t[cc][lane].x);
                 }
             }
             __syncthreads();
@@ -1142,15 +1309,30 @@ __global__ void __launch_bounds__(kScoreWarps * 32) score_kernel(int level, int3
             rec.score = fb;
         }
         ts->split[level] = rec;
+        s_bi[0] = fk;
+    }
+    if (small_side) {  // the next level builds, per leaf, the winner's lighter child
+        __syncthreads();
+        const int k = s_bi[0];
+        for (int q = threadIdx.x; q < Q; q += blockDim.x) {
+            uint8_t side = 1;
+            if (k != 0x7fffffff) {
+                const ull* row = cur + ((size_t)((k >> 8) - f0) * Q + q) * B * 2;
+                const ull fm = row[2 * (k & 255) + 1];
+                side = true_child_built(fm, row[2 * (B - 1) + 1] - fm);
+            }
+            small_side[q] = side;
+        }
     }
 }
 
 void launch_score(int level, int32_t Fs, int32_t f0, int32_t F, int32_t B, const ull* cur,
                   const int32_t* border_counts, double l2, int score_fn, double* grp_score, int32_t* grp_bin,
-                  TreeState* ts, ull* rank_best, cudaStream_t st) {
+                  TreeState* ts, ull* rank_best, uint8_t* small_side, cudaStream_t st) {
     const unsigned G = (unsigned)((B - 1 + 31) / 32);  // border groups: borders <= B - 1
     score_kernel<<<dim3(G > 0 ? G : 1, (unsigned)Fs), kScoreWarps * 32, 0, st>>>(
-        level, Fs, f0, F, B, cur, border_counts, l2, score_fn, grp_score, grp_bin, ts, rank_best);
+        level, Fs, f0, F, B, cur, border_counts, l2, score_fn, grp_score, grp_bin, ts, rank_best,
+        rank_best ? nullptr : small_side);
 }
 
 // The winner over the ranks' slice winners, gathered as (score bits, key,
@@ -1212,67 +1394,42 @@ __device__ __forceinline__ PartView part_view(const TreeState* ts, int level, co
 }
 
 // ============================================================================
-// partition by route-and-compact
+// partition: route and list in one pass
 // ============================================================================
 // After split l is chosen every row's leaf id gains bit l (routing,
 // tree.rs:1005-1016), and the next level needs, for each of its 2^l parents,
-// the rows of the child it builds (the one with fewer rows -- the CPU's
-// n_true <= n_false rule, tree.rs:1111 -- or the side the ranks agreed on; the
-// sibling is derived).  Three kernels and no pass over the previous level's
-// row order:
-//  route:   leaf[i] |= (bin[f][i] > b) << l over rows in natural order (16
-//           consecutive rows per thread, 16-byte loads), with per-child row
-//           counts (block-local shared counters, one atomic per (block,
-//           child));
-//  side:    the build side per parent, the built children's segments in
-//           parent order, and a cursor per segment;
-//  compact: each block writes its built-child rows, in row order, to a range
-//           of each segment reserved with one atomic per (block, segment).
-// Rows of a segment therefore appear in block-scheduling order; the
-// histograms, exact integer sums, do not depend on it.
+// the rows of the child it builds (the sibling is derived by subtraction,
+// tree.rs:1075-1131).  Which child is built changes no result -- the sums are
+// exact -- so the side is chosen before routing, from the split's (false,
+// true) weight sums that the score kernel (one GPU) or select_split (ranks)
+// already holds: the child with no more weight than its sibling.  Every
+// parent q owns a segment [base[q], base[q] + rows[q]) of the row list, laid
+// out in parent order from the parents' row counts, so its built child's
+// rows (at most rows[q]) fit without a counting pass.  Two kernels:
+//  partition: leaf[i] |= (bin[f][i] > b) << l over rows in natural order (16
+//             consecutive rows per thread, 16-byte loads); each block writes
+//             its built-child rows to a range of each parent's segment
+//             reserved with one atomic per (block, parent);
+//  segments:  the built children's extents become the next level's
+//             histogram work list; the 2^(l+1) children's row counts (built:
+//             listed rows; sibling: parent minus built) lay out the next
+//             partition's segments.
+// Rows of a segment appear in block-scheduling order; the histograms, exact
+// integer sums, do not depend on it.
 
 constexpr int kRouteThreads = 256;
 constexpr int kRouteRows = 16;  // consecutive rows per thread
 constexpr int kRouteTile = kRouteThreads * kRouteRows;
-constexpr int kRouteSmemChildren = 4096;  // deeper levels count with global atomics
-constexpr int kCompactSmemParents = 256;  // deeper levels reserve one slot per row
+constexpr int kPartSmemParents = 256;  // deeper levels reserve one slot per row
 
-// kNc > 0: the level has kNc <= 8 children, counted in registers and reduced
-// per warp (few distinct counters would serialize shared atomics); kNc == 0:
-// shared-memory counters (up to kRouteSmemChildren children), else global.
-template <int kNc>
-__global__ void __launch_bounds__(kRouteThreads) route_kernel(int level, int64_t n,
-                                                              const uint8_t* __restrict__ bins_fm, int64_t n_stride,
-                                                              const TreeState* __restrict__ ts,
-                                                              uint16_t* __restrict__ leaf,
-                                                              uint32_t* __restrict__ child_tot) {
-    __shared__ uint32_t s_cnt[kNc > 0 ? 8 : kRouteSmemChildren];
-    const int nc = 2 << level;
-    const bool count = child_tot != nullptr;
-    const bool smem = count && (kNc > 0 || nc <= kRouteSmemChildren);
-    if (smem) {
-        for (int k = threadIdx.x; k < (kNc > 0 ? kNc : nc); k += blockDim.x) s_cnt[k] = 0u;
-        __syncthreads();
-    }
-    const PartView pv = part_view(ts, level, bins_fm, n_stride);
-    const int64_t r0 = (int64_t)blockIdx.x * kRouteTile + (int64_t)threadIdx.x * kRouteRows;
-    uint32_t rc[kNc > 0 ? kNc : 1];
-#pragma unroll
-    for (int v = 0; v < (kNc > 0 ? kNc : 1); ++v) rc[v] = 0u;
-    auto tally = [&](uint32_t c) {
-        if (kNc > 0) {
-#pragma unroll
-            for (int v = 0; v < (kNc > 0 ? kNc : 1); ++v) rc[v] += c == (uint32_t)v ? 1u : 0u;
-        } else if (smem) {
-            atomicAdd(&s_cnt[c], 1u);
-        } else if (count) {
-            atomicAdd(&child_tot[c], 1u);
-        }
-    };
+// Leaf ids of the thread's 16 rows after split `level`: lv[k] = old id | side
+// << level (the old id is not read at level 0); written back.  Rows past n
+// get ~0.
+__device__ __forceinline__ void route_rows(int level, int64_t n, int64_t r0, const PartView& pv,
+                                           uint16_t* __restrict__ leaf, uint32_t (&lv)[kRouteRows]) {
     if (r0 + kRouteRows <= n) {
         const uint4 v = __ldg((const uint4*)(pv.col + r0));  // n_stride and r0 are multiples of 16
         const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-        uint32_t lv[kRouteRows];
         if (level > 0) {
             const uint4 a = ((const uint4*)(leaf + r0))[0], b = ((const uint4*)(leaf + r0))[1];
             const uint32_t p[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
@@ -1283,10 +1440,8 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(int level, int64_t
             for (int k = 0; k < kRouteRows; ++k) lv[k] = 0u;
         }
 #pragma unroll
-        for (int k = 0; k < kRouteRows; ++k) {
+        for (int k = 0; k < kRouteRows; ++k)
             lv[k] |= (uint32_t)((int32_t)((w[k >> 2] >> ((k & 3) * 8)) & 0xffu) > pv.bin) << level;
-            if (count) tally(lv[k]);
-        }
         uint4 o0, o1;
         o0.x = lv[0] | (lv[1] << 16); o0.y = lv[2] | (lv[3] << 16);
         o0.z = lv[4] | (lv[5] << 16); o0.w = lv[6] | (lv[7] << 16);
@@ -1295,106 +1450,48 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(int level, int64_t
         ((uint4*)(leaf + r0))[0] = o0;
         ((uint4*)(leaf + r0))[1] = o1;
     } else {
-        for (int64_t i = r0; i < n; ++i) {
-            const uint32_t c = (level > 0 ? (uint32_t)leaf[i] : 0u) |
-                               ((uint32_t)((int32_t)pv.col[i] > pv.bin) << level);
-            leaf[i] = (uint16_t)c;
-            if (count) tally(c);
-        }
-    }
-    if (kNc > 0 && count) {
 #pragma unroll
-        for (int v = 0; v < (kNc > 0 ? kNc : 1); ++v) {
-            uint32_t t = rc[v];
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(kFull, t, o);
-            if ((threadIdx.x & 31) == 0 && t) atomicAdd(&s_cnt[v], t);
+        for (int k = 0; k < kRouteRows; ++k) {
+            const int64_t i = r0 + k;
+            lv[k] = 0xffffffffu;
+            if (i < n) {
+                lv[k] = (level > 0 ? (uint32_t)leaf[i] : 0u) | ((uint32_t)((int32_t)pv.col[i] > pv.bin) << level);
+                leaf[i] = (uint16_t)lv[k];
+            }
         }
-    }
-    if (smem) {
-        __syncthreads();
-        for (int k = threadIdx.x; k < (kNc > 0 ? kNc : nc); k += blockDim.x)
-            if (s_cnt[k]) atomicAdd(&child_tot[k], s_cnt[k]);
     }
 }
 
-// One block: the build side of each of the Q = 2^level parents (decide: from
-// the child row counts; else the side already in small_side), the built
-// children's segments [seg_off, seg_off + cnt) in parent order with a write
-// cursor per parent, and the next level's histogram work list: each segment
-// cut into kChunkRows-row items, in parent order (cap items at most).
-__global__ void __launch_bounds__(1024) build_side_kernel(int level, int decide, const uint32_t* __restrict__ child_tot,
-                                                          uint8_t* __restrict__ small_side,
-                                                          uint32_t* __restrict__ cursor,
-                                                          HistChunk* __restrict__ chunks, uint32_t cap,
-                                                          uint32_t* __restrict__ n_chunks, TreeState* ts) {
-    __shared__ uint32_t s_scan[40];
-    const uint32_t Q = 1u << level;
-    const uint32_t per = (Q + blockDim.x - 1) / blockDim.x;
-    const uint32_t q0 = threadIdx.x * per;
-    const uint32_t cr = kChunkRows;
-    uint32_t rows = 0, items = 0;
-    for (uint32_t q = q0; q < q0 + per && q < Q; ++q) {
-        if (decide) small_side[q] = child_tot[q + Q] <= child_tot[q] ? 1 : 0;
-        const uint32_t cnt = child_tot[small_side[q] ? q + Q : q];
-        rows += cnt;
-        items += (cnt + cr - 1) / cr;
-    }
-    uint32_t rows_tot, items_tot;
-    uint32_t off = block_excl_scan<uint32_t>(rows, s_scan, &rows_tot);
-    uint32_t item = block_excl_scan<uint32_t>(items, s_scan, &items_tot);
-    for (uint32_t q = q0; q < q0 + per && q < Q; ++q) {
-        const uint32_t cnt = child_tot[small_side[q] ? q + Q : q];
-        cursor[q] = off;
-        for (uint32_t st = 0; st < cnt; st += cr) {
-            if (item < cap) chunks[item] = HistChunk{q, off + st, cnt - st < cr ? cnt - st : cr, 0u};
-            ++item;
-        }
-        off += cnt;
-    }
-    if (threadIdx.x == 0) {
-        if (items_tot > cap) {  // cannot happen with the session's sizing; never write past the buffer
-            atomicOr(&ts->err, kErrChunkCap);
-            items_tot = cap;
-        }
-        n_chunks[0] = items_tot;
-        ts->hist_rows[level + 1] = rows_tot;
-    }
-}
-
-// Blocks cover the route kernel's row tiles; thread t of a block owns its 16
-// consecutive rows (one 32-byte load of their leaf ids).  A row goes to its
-// parent's segment when its leaf is the built child.  Pass 1 ranks each row
-// among its warp's rows of the same parent (kQ > 0, at most 4 parents:
-// ballots per parent; kQ == 0: per-warp shared counters, at most
-// kCompactSmemParents parents), the block reserves one range per parent, pass
-// 2 writes the rows.
+// Route, then list the built-child rows.  A row goes to parent q's segment
+// when its new bit is the side small_side[q].  Ranks within the block: kQ > 0
+// (levels 0 and 1, kQ = 2^level parents) one ballot per (row, parent); kQ ==
+// 0 per-warp shared counters (at most kPartSmemParents parents), else one
+// global slot per row.  The block then reserves one range per parent and
+// writes its rows there.
 template <int kQ>
-__global__ void __launch_bounds__(kRouteThreads) compact_kernel(int level, int64_t n,
-                                                                const uint16_t* __restrict__ leaf,
-                                                                const uint8_t* __restrict__ small_side,
-                                                                uint32_t* __restrict__ cursor,
-                                                                uint32_t* __restrict__ list) {
+__global__ void __launch_bounds__(kRouteThreads, 4) partition_kernel(int level, int64_t n,
+                                                                     const uint8_t* __restrict__ bins_fm,
+                                                                     int64_t n_stride,
+                                                                     const TreeState* __restrict__ ts,
+                                                                     uint16_t* __restrict__ leaf,
+                                                                     const uint8_t* __restrict__ small_side,
+                                                                     uint32_t* __restrict__ cursor,
+                                                                     uint32_t* __restrict__ list) {
     constexpr int kWarps = kRouteThreads / 32;
-    constexpr int kP = kQ > 0 ? kQ : kCompactSmemParents;
+    constexpr int kP = kQ > 0 ? kQ : kPartSmemParents;
     __shared__ uint32_t s_w[kWarps][kP];  // per-warp counts, then write bases
     __shared__ uint8_t s_side[kP];
     const uint32_t Q = 1u << level;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int64_t r0 = (int64_t)blockIdx.x * kRouteTile + (int64_t)threadIdx.x * kRouteRows;
     const bool smem = Q <= (uint32_t)kP;
-    if (smem)
+    if (smem) {
         for (uint32_t q = threadIdx.x; q < Q; q += blockDim.x) s_side[q] = small_side[q];
-    uint32_t lv[kRouteRows];
-    if (r0 + kRouteRows <= n) {
-        const uint4 a = ((const uint4*)(leaf + r0))[0], b = ((const uint4*)(leaf + r0))[1];
-        const uint32_t p[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-#pragma unroll
-        for (int k = 0; k < kRouteRows; ++k) lv[k] = (p[k >> 1] >> ((k & 1) * 16)) & 0xffffu;
-    } else {
-#pragma unroll
-        for (int k = 0; k < kRouteRows; ++k) lv[k] = r0 + k < n ? (uint32_t)leaf[r0 + k] : 0xffffffffu;
+        for (uint32_t k = threadIdx.x; k < kWarps * Q; k += blockDim.x) s_w[k >> level][k & (Q - 1u)] = 0u;
     }
+    const PartView pv = part_view(ts, level, bins_fm, n_stride);
+    const int64_t r0 = (int64_t)blockIdx.x * kRouteTile + (int64_t)threadIdx.x * kRouteRows;
+    uint32_t lv[kRouteRows];
+    route_rows(level, n, r0, pv, leaf, lv);
     if (!smem) {  // deep levels: one reserved slot per row
 #pragma unroll
         for (int k = 0; k < kRouteRows; ++k) {
@@ -1404,30 +1501,30 @@ __global__ void __launch_bounds__(kRouteThreads) compact_kernel(int level, int64
         }
         return;
     }
-    for (uint32_t k = threadIdx.x; k < kWarps * Q; k += blockDim.x) s_w[k / Q][k % Q] = 0u;
     __syncthreads();
-    uint32_t par[kRouteRows];  // parent of row r0 + k, or ~0 when the row is not listed
+    // per row: parent << 16 | rank among the warp's rows of that parent (a
+    // warp has 512 rows), or ~0 when the row is not listed
+    uint32_t pr[kRouteRows];
 #pragma unroll
     for (int k = 0; k < kRouteRows; ++k) {
-        par[k] = 0xffffffffu;
+        pr[k] = 0xffffffffu;
         if (lv[k] != 0xffffffffu) {
             const uint32_t q = lv[k] & (Q - 1u);
-            if ((lv[k] >> level) == (uint32_t)s_side[q]) par[k] = q;
+            if ((lv[k] >> level) == (uint32_t)s_side[q]) pr[k] = q << 16;
         }
     }
-    const uint32_t lt = (1u << lane) - 1u;
-    uint32_t rank[kRouteRows];
     if (kQ > 0) {
+        const uint32_t lt = (1u << lane) - 1u;
         uint32_t run[kQ > 0 ? kQ : 1];
 #pragma unroll
         for (int v = 0; v < (kQ > 0 ? kQ : 1); ++v) run[v] = 0u;
 #pragma unroll
         for (int k = 0; k < kRouteRows; ++k) {
-            rank[k] = 0u;
 #pragma unroll
             for (int v = 0; v < (kQ > 0 ? kQ : 1); ++v) {
-                const uint32_t m = __ballot_sync(kFull, par[k] == (uint32_t)v);
-                if (par[k] == (uint32_t)v) rank[k] = run[v] + (uint32_t)__popc(m & lt);
+                const bool mine = pr[k] == ((uint32_t)v << 16);
+                const uint32_t m = __ballot_sync(kFull, mine);
+                if (mine) pr[k] |= run[v] + (uint32_t)__popc(m & lt);
                 run[v] += (uint32_t)__popc(m);
             }
         }
@@ -1439,7 +1536,7 @@ __global__ void __launch_bounds__(kRouteThreads) compact_kernel(int level, int64
     } else {
 #pragma unroll
         for (int k = 0; k < kRouteRows; ++k)
-            rank[k] = par[k] != 0xffffffffu ? atomicAdd(&s_w[warp][par[k]], 1u) : 0u;
+            if (pr[k] != 0xffffffffu) pr[k] |= atomicAdd(&s_w[warp][pr[k] >> 16], 1u);
     }
     __syncthreads();
     for (uint32_t q = threadIdx.x; q < Q; q += blockDim.x) {
@@ -1455,77 +1552,184 @@ __global__ void __launch_bounds__(kRouteThreads) compact_kernel(int level, int64
     __syncthreads();
 #pragma unroll
     for (int k = 0; k < kRouteRows; ++k)
-        if (par[k] != 0xffffffffu) list[s_w[warp][par[k]] + rank[k]] = (uint32_t)(r0 + k);
+        if (pr[k] != 0xffffffffu) list[s_w[warp][pr[k] >> 16] + (pr[k] & 0xffffu)] = (uint32_t)(r0 + k);
 }
 
-void launch_route(int level, int64_t n, const uint8_t* bins_fm, int64_t n_stride, uint16_t* leaf,
-                  uint32_t* child_tot, TreeState* ts, cudaStream_t st) {
+// One block, after the partition of split `level` (Q = 2^level parents):
+// parent q's built child holds cursor[q] - base[q] listed rows (rows_in null:
+// one parent of n rows; base_in null: base 0).  Writes the next level's
+// histogram work list (each built segment cut into kChunkRows-row items, in
+// parent order, cap items at most) and ts->hist_rows[level + 1]; when rows_out
+// is not null, the 2Q children's row counts (child q + side * Q) with their
+// segments (exclusive prefix in child order) as rows_out / base_out, and
+// cursor_out = base_out for the next partition.
+__global__ void __launch_bounds__(1024) segments_kernel(int level, int64_t n, const uint32_t* __restrict__ rows_in,
+                                                        const uint32_t* __restrict__ base_in,
+                                                        const uint32_t* __restrict__ cursor,
+                                                        const uint8_t* __restrict__ small_side,
+                                                        uint32_t* __restrict__ rows_out, uint32_t* __restrict__ base_out,
+                                                        uint32_t* __restrict__ cursor_out, HistChunk* __restrict__ chunks,
+                                                        uint32_t cap, uint32_t* __restrict__ n_chunks, TreeState* ts) {
+    __shared__ uint32_t s_scan[40];
+    const uint32_t Q = 1u << level;
+    const uint32_t per = (Q + blockDim.x - 1) / blockDim.x;
+    const uint32_t q0 = threadIdx.x * per;
+    const uint32_t cr = kChunkRows;
+    auto base_of = [&](uint32_t q) { return base_in ? base_in[q] : 0u; };
+    uint32_t rows = 0, items = 0;
+    for (uint32_t q = q0; q < q0 + per && q < Q; ++q) {
+        const uint32_t cnt = cursor[q] - base_of(q);
+        rows += cnt;
+        items += (cnt + cr - 1) / cr;
+    }
+    uint32_t rows_tot, items_tot;
+    (void)block_excl_scan<uint32_t>(rows, s_scan, &rows_tot);
+    uint32_t item = block_excl_scan<uint32_t>(items, s_scan, &items_tot);
+    for (uint32_t q = q0; q < q0 + per && q < Q; ++q) {
+        const uint32_t b = base_of(q), cnt = cursor[q] - b;
+        for (uint32_t st = 0; st < cnt; st += cr) {
+            if (item < cap) chunks[item] = HistChunk{q, b + st, cnt - st < cr ? cnt - st : cr, 0u};
+            ++item;
+        }
+    }
+    if (threadIdx.x == 0) {
+        if (items_tot > cap) {  // cannot happen with the session's sizing; never write past the buffer
+            atomicOr(&ts->err, kErrChunkCap);
+            items_tot = cap;
+        }
+        n_chunks[0] = items_tot;
+        ts->hist_rows[level + 1] = rows_tot;
+    }
+    if (!rows_out) return;
+    // children j < 2Q in order: j = q + side * Q
+    const uint32_t per2 = (2 * Q + blockDim.x - 1) / blockDim.x;
+    const uint32_t j0 = threadIdx.x * per2;
+    auto child_rows = [&](uint32_t j) {
+        const uint32_t q = j & (Q - 1u), side = j >> level;
+        const uint32_t built = cursor[q] - base_of(q);
+        const uint32_t parent = rows_in ? rows_in[q] : (uint32_t)n;
+        return side == (uint32_t)small_side[q] ? built : parent - built;
+    };
+    uint32_t sum = 0;
+    for (uint32_t j = j0; j < j0 + per2 && j < 2 * Q; ++j) sum += child_rows(j);
+    uint32_t off = block_excl_scan<uint32_t>(sum, s_scan, nullptr);
+    for (uint32_t j = j0; j < j0 + per2 && j < 2 * Q; ++j) {
+        const uint32_t c = child_rows(j);
+        rows_out[j] = c;
+        base_out[j] = off;
+        cursor_out[j] = off;
+        off += c;
+    }
+}
+
+void launch_partition(int level, int64_t n, const uint8_t* bins_fm, int64_t n_stride, uint16_t* leaf,
+                      const uint8_t* small_side, uint32_t* cursor, uint32_t* list, TreeState* ts, cudaStream_t st) {
     const int64_t tiles = (n + kRouteTile - 1) / kRouteTile;
     if (tiles <= 0) return;
     const unsigned g = (unsigned)tiles;
-    if (child_tot && level == 0) route_kernel<2><<<g, kRouteThreads, 0, st>>>(level, n, bins_fm, n_stride, ts, leaf, child_tot);
-    else if (child_tot && level == 1) route_kernel<4><<<g, kRouteThreads, 0, st>>>(level, n, bins_fm, n_stride, ts, leaf, child_tot);
-    else if (child_tot && level == 2) route_kernel<8><<<g, kRouteThreads, 0, st>>>(level, n, bins_fm, n_stride, ts, leaf, child_tot);
-    else route_kernel<0><<<g, kRouteThreads, 0, st>>>(level, n, bins_fm, n_stride, ts, leaf, child_tot);
+    if (level == 0)
+        partition_kernel<1><<<g, kRouteThreads, 0, st>>>(level, n, bins_fm, n_stride, ts, leaf, small_side, cursor, list);
+    else if (level == 1)
+        partition_kernel<2><<<g, kRouteThreads, 0, st>>>(level, n, bins_fm, n_stride, ts, leaf, small_side, cursor, list);
+    else
+        partition_kernel<0><<<g, kRouteThreads, 0, st>>>(level, n, bins_fm, n_stride, ts, leaf, small_side, cursor, list);
 }
 
-void launch_build_side(int level, bool decide, const uint32_t* child_tot, uint8_t* small_side, uint32_t* cursor,
-                       HistChunk* chunks, uint32_t cap, uint32_t* n_chunks, TreeState* ts, cudaStream_t st) {
-    build_side_kernel<<<1, 1024, 0, st>>>(level, decide ? 1 : 0, child_tot, small_side, cursor, chunks, cap,
-                                          n_chunks, ts);
-}
-
-void launch_compact(int level, int64_t n, const uint16_t* leaf, const uint8_t* small_side, uint32_t* cursor,
-                    uint32_t* list, cudaStream_t st) {
-    const int64_t tiles = (n + kRouteTile - 1) / kRouteTile;
-    if (tiles <= 0) return;
-    const unsigned g = (unsigned)tiles;
-    if (level == 0) compact_kernel<1><<<g, kRouteThreads, 0, st>>>(level, n, leaf, small_side, cursor, list);
-    else if (level == 1) compact_kernel<2><<<g, kRouteThreads, 0, st>>>(level, n, leaf, small_side, cursor, list);
-    else if (level == 2) compact_kernel<4><<<g, kRouteThreads, 0, st>>>(level, n, leaf, small_side, cursor, list);
-    else compact_kernel<0><<<g, kRouteThreads, 0, st>>>(level, n, leaf, small_side, cursor, list);
+void launch_segments(int level, int64_t n, const uint32_t* rows_in, const uint32_t* base_in, const uint32_t* cursor,
+                     const uint8_t* small_side, uint32_t* rows_out, uint32_t* base_out, uint32_t* cursor_out,
+                     HistChunk* chunks, uint32_t cap, uint32_t* n_chunks, TreeState* ts, cudaStream_t st) {
+    segments_kernel<<<1, 1024, 0, st>>>(level, n, rows_in, base_in, cursor, small_side, rows_out, base_out,
+                                        cursor_out, chunks, cap, n_chunks, ts);
 }
 
 // ============================================================================
-// last level: final leaf id of every row (natural order), then the unsampled
-// leaf sums (boosting.rs:2470-2517 Gradient leaves over the full w*der1 / w
-// channels) as exact int64 sums.
+// last split: the final leaf id of every row (natural order) and, in the same
+// pass, the unsampled leaf sums (boosting.rs:2470-2517 Gradient leaves over
+// the full w*der1 / w channels) as exact int64 sums.
 // ============================================================================
-__global__ void __launch_bounds__(256) leafsum_kernel(int64_t n, const uint16_t* __restrict__ leaf,
-                                                      const double* __restrict__ wd1,
-                                                      const double* __restrict__ weight, int depth,
-                                                      const TreeState* __restrict__ ts,
-                                                      ull* __restrict__ leaf_sums) {
-    extern __shared__ ull lsm[];
-    const int L = 1 << depth;
-    const bool use_smem = depth <= 10;
-    if (use_smem) {
-        for (int k = threadIdx.x; k < 2 * L; k += blockDim.x) lsm[k] = 0ull;
+constexpr int kLeafSmemDepth = 10;  // deeper trees add into the global sums per row
+constexpr int kLeafsumBlocksPerSm = 4;
+
+// Exact 64-bit add into a shared (lo, hi) u32 pair: the lo add's wrap carries
+// into hi, so hi * 2^32 + lo is the sum mod 2^64 (the true sum fits an int64).
+__device__ __forceinline__ void add_split64(uint32_t* lo, uint32_t* hi, long long v) {
+    const uint32_t l = (uint32_t)(unsigned long long)v;
+    const uint32_t old = atomicAdd(lo, l);
+    atomicAdd(hi, (uint32_t)(v >> 32) + (old + l < old ? 1u : 0u));
+}
+
+__global__ void __launch_bounds__(kRouteThreads) route_leafsum_kernel(int level, int64_t n,
+                                                                      const uint8_t* __restrict__ bins_fm,
+                                                                      int64_t n_stride,
+                                                                      const TreeState* __restrict__ ts,
+                                                                      uint16_t* __restrict__ leaf,
+                                                                      const double* __restrict__ wd1,
+                                                                      const double* __restrict__ weight,
+                                                                      ull* __restrict__ leaf_sums) {
+    // shared: [L] lo and [L] hi of w*der1, then of w (with weights) or [L] row
+    // counts (without: every row adds the same fixed-point 1)
+    extern __shared__ uint32_t lsm[];
+    const int L = 2 << level;
+    const bool smem = level + 1 <= kLeafSmemDepth;
+    const int parts = weight ? 4 : 3;
+    if (smem) {
+        for (int k = threadIdx.x; k < parts * L; k += blockDim.x) lsm[k] = 0u;
         __syncthreads();
     }
     const Pow2 sd = ts->sc.scale[2], sw = ts->sc.scale[3];
-    ull* acc = use_smem ? lsm : leaf_sums;
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        const uint32_t q = leaf[i];
-        const double w = weight ? weight[i] : 1.0;
-        atomicAdd(acc + 2 * q, (ull)to_fixed(wd1[i], sd));
-        atomicAdd(acc + 2 * q + 1, (ull)to_fixed(w, sw));
+    const long long one = to_fixed(1.0, sw);
+    const PartView pv = part_view(ts, level, bins_fm, n_stride);
+    const int64_t tiles = (n + kRouteTile - 1) / kRouteTile;
+    for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
+        const int64_t r0 = t * kRouteTile + (int64_t)threadIdx.x * kRouteRows;
+        uint32_t lv[kRouteRows];
+        route_rows(level, n, r0, pv, leaf, lv);
+        double d[kRouteRows];
+        if (r0 + kRouteRows <= n) {
+#pragma unroll
+            for (int k = 0; k < kRouteRows; k += 2) {
+                const double2 v = *(const double2*)(wd1 + r0 + k);  // r0 is a multiple of 16 rows
+                d[k] = v.x;
+                d[k + 1] = v.y;
+            }
+        } else {
+#pragma unroll
+            for (int k = 0; k < kRouteRows; ++k) d[k] = r0 + k < n ? wd1[r0 + k] : 0.0;
+        }
+#pragma unroll
+        for (int k = 0; k < kRouteRows; ++k) {
+            if (lv[k] == 0xffffffffu) continue;
+            const uint32_t q = lv[k];
+            const long long vd = to_fixed(d[k], sd);
+            if (smem) {
+                add_split64(lsm + q, lsm + L + q, vd);
+                if (weight) add_split64(lsm + 2 * L + q, lsm + 3 * L + q, to_fixed(weight[r0 + k], sw));
+                else atomicAdd(lsm + 2 * L + q, 1u);
+            } else {
+                atomicAdd(leaf_sums + 2 * q, (ull)vd);
+                atomicAdd(leaf_sums + 2 * q + 1, (ull)(weight ? to_fixed(weight[r0 + k], sw) : one));
+            }
+        }
     }
-    if (use_smem) {
-        __syncthreads();
-        for (int k = threadIdx.x; k < 2 * L; k += blockDim.x)
-            if (lsm[k]) atomicAdd(leaf_sums + k, lsm[k]);
+    if (!smem) return;
+    __syncthreads();
+    for (int q = threadIdx.x; q < L; q += blockDim.x) {
+        const ull sdv = ((ull)lsm[L + q] << 32) + lsm[q];
+        const ull swv = weight ? ((ull)lsm[3 * L + q] << 32) + lsm[2 * L + q]
+                               : (ull)lsm[2 * L + q] * (ull)one;
+        if (sdv) atomicAdd(leaf_sums + 2 * q, sdv);
+        if (swv) atomicAdd(leaf_sums + 2 * q + 1, swv);
     }
 }
 
-void launch_leafsum(int depth, int64_t n, const uint16_t* leaf, const double* wd1, const double* weight,
-                    TreeState* ts, ull* leaf_sums, cudaStream_t st) {
-    if (n <= 0) return;
-    int64_t blocks = (n + 255) / 256;
-    if (blocks > 148 * 4) blocks = 148 * 4;
-    const size_t smem = depth <= 10 ? sizeof(ull) * 2 * (1 << depth) : 0;
-    leafsum_kernel<<<(unsigned)blocks, 256, smem, st>>>(n, leaf, wd1, weight, depth, ts, leaf_sums);
+void launch_route_leafsum(int level, int64_t n, const uint8_t* bins_fm, int64_t n_stride, uint16_t* leaf,
+                          const double* wd1, const double* weight, TreeState* ts, ull* leaf_sums, cudaStream_t st) {
+    const int64_t tiles = (n + kRouteTile - 1) / kRouteTile;
+    if (tiles <= 0) return;
+    int64_t blocks = tiles < 148 * kLeafsumBlocksPerSm ? tiles : 148 * kLeafsumBlocksPerSm;
+    const size_t smem = level + 1 <= kLeafSmemDepth ? sizeof(uint32_t) * (weight ? 4 : 3) * ((size_t)2 << level) : 0;
+    route_leafsum_kernel<<<(unsigned)blocks, kRouteThreads, smem, st>>>(level, n, bins_fm, n_stride, ts, leaf, wd1,
+                                                                        weight, leaf_sums);
 }
 
 // Gradient leaf delta calc_average(sum w*der1, sum w, scaled_l2) (leaf.rs:161-199),

@@ -101,7 +101,8 @@ struct TreeState {
     SplitRec split[16];
     uint32_t err;
     uint32_t score_done;   // last-block-done counter of the score kernel
-    uint32_t pad[2];
+    uint32_t cursor0;      // write cursor of the first partition's one segment
+    uint32_t pad;
     uint32_t hist_rows[16];  // rows histogrammed at each level (the smaller children)
     ull maxbits[4];        // bit patterns of max |channel| (non-negative doubles)
     Scales sc;
@@ -110,6 +111,7 @@ struct TreeState {
 constexpr int kTile = 32;          // features per histogram tile (one per lane)
 constexpr int kHistSmemMax = 227 * 1024;  // dynamic shared memory opt-in limit per block
 constexpr int kChunkRows = 16384;  // rows per histogram work item
+constexpr int kSegMax = 1 << 15;   // parents or children of one partition (depth <= 16)
 // Score-channel fixed point: |row value| <= 2^kPackBits, split at bit kPackSplit
 // into (lo, hi) u32 parts whose sums over kChunkRows rows stay below 2^31.
 constexpr int kPackBits = 33;
@@ -128,7 +130,8 @@ CBGPU_HD uint4 pack_gh(double g, double h, Pow2 sg, Pow2 sh) {
     o.w = (uint32_t)(int32_t)(qh >> kPackSplit);
     return o;
 }
-constexpr int kBootRun = 8;        // consecutive rows per thread in the bootstrap kernel
+constexpr int kBootRun = 8;        // consecutive rows per thread in the bootstrap and derivative kernels
+constexpr int kJumpSteps = 1010;   // LCG jump table: Bayesian jumps are 10 + (row mod 1000) steps
 
 // ---- multi-rank decisions (host and device share this code) ----------------
 //
@@ -178,10 +181,13 @@ CBGPU_HD int pick_split(const unsigned long long* all_best, int world, int strid
 // the true child) when the true child carries no more weight than the false
 // one.  Which child is built changes no result -- the sums are exact -- so
 // every rank only needs the same answer.
+CBGPU_HD uint8_t true_child_built(unsigned long long false_w, unsigned long long true_w) {
+    return true_w <= false_w ? 1 : 0;
+}
 CBGPU_HD uint8_t build_true_side(const unsigned long long* winner_rec, int q) {
     if (!winner_rec) return 1;
     const unsigned long long* m = winner_rec + 2;
-    return m[2 * q + 1] <= m[2 * q] ? 1 : 0;
+    return true_child_built(m[2 * q], m[2 * q + 1]);
 }
 
 // cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (kernel, device)
@@ -205,11 +211,17 @@ void launch_bootstrap(int mode, int64_t n, int64_t row_offset, const TreeParams*
 // MVS with lambda tp->mvs_lambda and seed tp->boot_seed
 void launch_mvs(int64_t n, int64_t row_offset, const double* wd1, const TreeParams* tp, double rate,
                 double* thresholds, float* out_sw, cudaStream_t st);
+// The jump multipliers of 0 .. kJumpSteps - 1 LCG steps (2 * kJumpSteps words).
+void launch_jump_table(ull* jump, cudaStream_t st);
 // s_mode: 0 = none (weights 1), 1 = f32 device sample, 2 = f64 host sample.
-// approx += lrv[leaf] first when tp->pending.
+// approx += lrv[leaf] first when tp->pending.  boot_mode 1 / 2 draws the
+// Bayesian (temp) / Bernoulli (rate) sample in the same pass (as
+// launch_bootstrap, using the jump table when not null) into sw32 and uses
+// it (s_mode 1).
 void launch_der(int64_t n, int loss, double* approx, const double* target, const double* weight,
-                const uint16_t* leaf, const double* lrv, const TreeParams* tp, int s_mode, const float* sw32,
-                const double* sw64, double* wd1, TreeState* ts, bool defer_gh, cudaStream_t st);
+                const uint16_t* leaf, const double* lrv, const TreeParams* tp, int s_mode, float* sw32,
+                const double* sw64, double* wd1, TreeState* ts, bool defer_gh, int boot_mode, int64_t row_offset,
+                double rate, float temp, const ull* jump, cudaStream_t st);
 void launch_max_gh(int64_t n, const double* wd1, const double* weight, const float* sw32, TreeState* ts,
                    cudaStream_t st);
 // also records this rank's level-0 row count in ts->hist_rows[0]
@@ -232,33 +244,37 @@ void launch_level0_chunks(int64_t n, HistChunk* chunks, uint32_t cap, uint32_t* 
                           cudaStream_t st);
 // Derive and score work on this rank's feature slice [f0, f0 + Fs) in
 // feature-major layouts (see derive_prefix_kernel).  With rank_best null the
-// winner goes to ts->split[level]; otherwise the slice winner's record goes to
-// rank_best (score bits, key, then 2^level (false, true) weight sums) for
-// launch_select_split after an all-gather (records of `stride` words; a null
-// small_side skips the next level's build-side choice).
+// winner goes to ts->split[level] and, with small_side not null, each leaf's
+// build side for the next level (the winner's child with no more weight);
+// otherwise the slice winner's record goes to rank_best (score bits, key, then
+// 2^level (false, true) weight sums) for launch_select_split after an
+// all-gather (records of `stride` words; a null small_side skips the next
+// level's build-side choice).
 void launch_derive_prefix(int level, int32_t Fs, int32_t B, const ull* built, const ull* prev,
                           ull* cur, const uint8_t* small_side, cudaStream_t st);
 void launch_score(int level, int32_t Fs, int32_t f0, int32_t F, int32_t B, const ull* cur,
                   const int32_t* border_counts, double l2, int score_fn, double* grp_score, int32_t* grp_bin,
-                  TreeState* ts, ull* rank_best, cudaStream_t st);
+                  TreeState* ts, ull* rank_best, uint8_t* small_side, cudaStream_t st);
 void launch_select_split(int level, int world, int stride, const ull* all_best, TreeState* ts,
                          uint8_t* small_side, cudaStream_t st);
-// Routing by split `level` (leaf[i] |= (bin > border) << level; leaf[] is not
-// read at level 0), with per-child row counts added into child_tot[2 << level]
-// when child_tot is not null.
-void launch_route(int level, int64_t n, const uint8_t* bins_fm, int64_t n_stride, uint16_t* leaf,
-                  uint32_t* child_tot, TreeState* ts, cudaStream_t st);
-// The build side of each parent (decide: from child_tot; else small_side as
-// given), per-parent write cursors [2^level] of the built children's
-// segments, and the next level's histogram work list (ts->hist_rows[level + 1]).
-void launch_build_side(int level, bool decide, const uint32_t* child_tot, uint8_t* small_side, uint32_t* cursor,
-                       HistChunk* chunks, uint32_t cap, uint32_t* n_chunks, TreeState* ts, cudaStream_t st);
-// The rows of each parent's built child into list, at the cursors build_side set.
-void launch_compact(int level, int64_t n, const uint16_t* leaf, const uint8_t* small_side, uint32_t* cursor,
-                    uint32_t* list, cudaStream_t st);
-// Exact int64 sums of the unsampled w * der1 and w per final leaf.
-void launch_leafsum(int depth, int64_t n, const uint16_t* leaf, const double* wd1, const double* weight,
-                    TreeState* ts, ull* leaf_sums, cudaStream_t st);
+// Routing by split `level` (leaf[] is not read at level 0) and, for each
+// parent q < 2^level, the rows of its built child (new bit == small_side[q])
+// written to list from cursor[q] on (cursor[q] advances past them).
+void launch_partition(int level, int64_t n, const uint8_t* bins_fm, int64_t n_stride, uint16_t* leaf,
+                      const uint8_t* small_side, uint32_t* cursor, uint32_t* list, TreeState* ts, cudaStream_t st);
+// After launch_partition(level): the next level's histogram work list from
+// the built segments [base_in[q], cursor[q]) (ts->hist_rows[level + 1]); with
+// rows_out not null, the 2^(level+1) children's row counts and segment starts
+// (rows_out, base_out, cursor_out = base_out) for the next partition.
+// rows_in / base_in null: level 0's single parent of n rows at base 0.
+void launch_segments(int level, int64_t n, const uint32_t* rows_in, const uint32_t* base_in, const uint32_t* cursor,
+                     const uint8_t* small_side, uint32_t* rows_out, uint32_t* base_out, uint32_t* cursor_out,
+                     HistChunk* chunks, uint32_t cap, uint32_t* n_chunks, TreeState* ts, cudaStream_t st);
+// The last split (`level`): leaf[i] |= (bin > border) << level, and the exact
+// int64 sums of the unsampled w * der1 and w per final leaf added into
+// leaf_sums[2 << level][2].
+void launch_route_leafsum(int level, int64_t n, const uint8_t* bins_fm, int64_t n_stride, uint16_t* leaf,
+                          const double* wd1, const double* weight, TreeState* ts, ull* leaf_sums, cudaStream_t st);
 // Exact leaves (MAE / Quantile): keys[i] = leaf << 32 | total-order bits of
 // the f32 residual, sorted with the weights, then one block per leaf takes
 // the weighted alpha-quantile into leaf_raw / leaf_lrv.  tmp / tmp_bytes is

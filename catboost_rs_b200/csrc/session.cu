@@ -166,12 +166,16 @@ struct cbgpu_session {
     double* mvs_thr = nullptr;
     uint16_t* leaf = nullptr;     // every row's leaf id (routed level by level; final after the tree)
     uint32_t* list = nullptr;     // the rows of each parent's built child, segment by segment
-    uint32_t* cursor = nullptr;   // per-parent write cursor into list
-    uint32_t* child_cnt = nullptr;
-    uint8_t* small_side = nullptr;
+    // per parent of a partition, two levels ([2][kSegMax], by level parity):
+    // write cursor into list, row count, segment start
+    uint32_t* cursor = nullptr;
+    uint32_t* seg_rows = nullptr;
+    uint32_t* seg_base = nullptr;
+    uint8_t* small_side = nullptr;  // per parent: 1 = the true child is built
+    ull* jump = nullptr;            // LCG jump multipliers (launch_jump_table)
     HistChunk* chunks0 = nullptr;  // level-0 work list (all rows), built at begin
     uint32_t* n_chunks0 = nullptr;
-    HistChunk* chunks = nullptr;   // the next level's work list, built by build_side
+    HistChunk* chunks = nullptr;   // the next level's work list, built by launch_segments
     size_t chunk_cap = 0;
     uint32_t* n_chunks = nullptr;
     ull* built = nullptr;
@@ -322,9 +326,11 @@ int alloc_session(cbgpu_session* s, const cbgpu_begin_args* a) {
     DA(s->mvs_thr, (n + 8191) / 8192);
     DA(s->leaf, n);
     DA(s->list, n);
-    DA(s->cursor, 1 << 15);     // up to 2^15 parents before the last split
-    DA(s->child_cnt, 1 << 16);
-    DA(s->small_side, 1 << 15);
+    DA(s->cursor, 2 * kSegMax);  // up to 2^15 parents per partition (depth <= 16)
+    DA(s->seg_rows, 2 * kSegMax);
+    DA(s->seg_base, 2 * kSegMax);
+    DA(s->small_side, kSegMax);
+    DA(s->jump, 2 * kJumpSteps);
     // full chunks plus one partial chunk per segment
     s->chunk_cap = (size_t)(n / kChunkRows) + (L / 2) + 2;
     DA(s->chunks, s->chunk_cap);
@@ -398,7 +404,7 @@ void free_session(cbgpu_session* s) {
         if (g) cudaGraphExecDestroy(g);
     void* ptrs[] = {s->bins_rm, s->bins_fm, s->d_border_counts, s->target, s->weight, s->approx,
                     s->wd1, s->qstats, s->sw32, s->sw64, s->mvs_thr, s->leaf, s->list, s->cursor,
-                    s->child_cnt, s->small_side, s->chunks0, s->n_chunks0, s->chunks, s->n_chunks, s->built,
+                    s->seg_rows, s->seg_base, s->small_side, s->jump, s->chunks0, s->n_chunks0, s->chunks, s->n_chunks, s->built,
                     s->hist[0], s->hist[1], s->feat_score, s->feat_bin, s->best_all, s->leaf_sums, s->leaf_raw,
                     s->leaf_lrv, s->ts, s->d_err, s->leaf_export, s->d_tp, s->ex_keys, s->ex_keys_sorted,
                     s->ex_w, s->ex_w_sorted, s->ex_tmp};
@@ -428,6 +434,7 @@ int finish_begin(cbgpu_session* s) {
     CU(cudaMemcpyAsync(s->d_border_counts, s->border_counts.data(), sizeof(int32_t) * s->F,
                        cudaMemcpyHostToDevice, s->st));
     if (s->n > 0) launch_transpose_fm_to_rm(s->bins_fm, s->n, s->n_stride, s->F, s->bins_rm, s->F_pad, s->st);
+    launch_jump_table(s->jump, s->st);
     launch_level0_chunks(s->n, s->chunks0, (uint32_t)(s->n / kChunkRows) + 2, s->n_chunks0, s->d_err, s->st);
     uint32_t herr = 0;
     CU(cudaMemcpyAsync(&herr, s->d_err, sizeof(uint32_t), cudaMemcpyDeviceToHost, s->st));
@@ -568,15 +575,10 @@ int enqueue_tree(cbgpu_session* s, int set, bool prof, int boot_mode, int s_mode
     };
     rec(0);
     CU(cudaMemsetAsync(s->ts, 0, sizeof(TreeState), st));
-    if (boot_mode == 1) {
-        launch_bootstrap(1, s->n, s->row_offset, s->d_tp, 0.0, s->temp, s->sw32, st);
-        ++launches;
-    } else if (boot_mode == 2) {
-        launch_bootstrap(2, s->n, s->row_offset, s->d_tp, (double)s->sample_rate, 0.0f, s->sw32, st);
-        ++launches;
-    }
+    // the Bayesian / Bernoulli sample is drawn inside the derivative pass
     launch_der(s->n, s->loss, s->approx, s->target, s->weight, s->leaf, s->leaf_lrv, s->d_tp, s_mode, s->sw32,
-               s->sw64, s->wd1, s->ts, mvs, st);
+               s->sw64, s->wd1, s->ts, mvs, boot_mode, s->row_offset, boot_mode == 2 ? (double)s->sample_rate : 0.0,
+               boot_mode == 1 ? s->temp : 0.0f, s->jump, st);
     ++launches;
     if (mvs) {
         launch_mvs(s->n, s->row_offset, s->wd1, s->d_tp, (double)s->sample_rate, s->mvs_thr, s->sw32, st);
@@ -620,7 +622,8 @@ int enqueue_tree(cbgpu_session* s, int set, bool prof, int boot_mode, int s_mode
         const int stride = 2 + 2 * (1 << l);  // all-gather record: score, key, (false, true) per leaf
         launch_score(l, s->Fs, s->f0, s->F, s->B, s->hist[cur], s->d_border_counts, s->l2, s->score_fn,
                      s->feat_score, s->feat_bin, s->ts,
-                     s->world > 1 ? s->best_all + (size_t)stride * s->rank : nullptr, st);
+                     s->world > 1 ? s->best_all + (size_t)stride * s->rank : nullptr,
+                     l + 1 < D ? s->small_side : nullptr, st);
         launches += 2;
         if (s->world > 1) {
             int rc = all_gather_u64(s, s->best_all, (size_t)stride);
@@ -631,21 +634,27 @@ int enqueue_tree(cbgpu_session* s, int set, bool prof, int boot_mode, int s_mode
         }
         rec(e + 3);
         if (l + 1 < D) {
-            // route every row, then list the rows of each parent's built child
-            // (single GPU: the child with fewer rows; multi-rank fits chose the
-            // side in select_split from the global weights)
-            CU(cudaMemsetAsync(s->child_cnt, 0, sizeof(uint32_t) * ((size_t)2 << l), st));
-            launch_route(l, s->n, s->bins_fm, s->n_stride, s->leaf, s->child_cnt, s->ts, st);
-            launch_build_side(l, s->world == 1, s->child_cnt, s->small_side, s->cursor, s->chunks,
-                              (uint32_t)s->chunk_cap, s->n_chunks, s->ts, st);
-            launch_compact(l, s->n, s->leaf, s->small_side, s->cursor, s->list, st);
+            // route every row and list the rows of each parent's built child
+            // (the side the score kernel or select_split chose from the
+            // split's weights), then the next level's work list and segments
+            const int p = l & 1, np = p ^ 1;
+            uint32_t* cur_l = l == 0 ? (uint32_t*)((char*)s->ts + offsetof(TreeState, cursor0))
+                                     : s->cursor + (size_t)p * kSegMax;
+            const bool more = l + 2 < D;  // another partition follows
+            launch_partition(l, s->n, s->bins_fm, s->n_stride, s->leaf, s->small_side, cur_l, s->list, s->ts, st);
+            launch_segments(l, s->n, l == 0 ? nullptr : s->seg_rows + (size_t)p * kSegMax,
+                            l == 0 ? nullptr : s->seg_base + (size_t)p * kSegMax, cur_l, s->small_side,
+                            more ? s->seg_rows + (size_t)np * kSegMax : nullptr,
+                            more ? s->seg_base + (size_t)np * kSegMax : nullptr,
+                            more ? s->cursor + (size_t)np * kSegMax : nullptr, s->chunks,
+                            (uint32_t)s->chunk_cap, s->n_chunks, s->ts, st);
             rec(e + 4);
-            launches += 3;
+            launches += 2;
         } else {
             CU(cudaMemsetAsync(s->leaf_sums, 0, sizeof(ull) * 2 * L, st));
-            launch_route(l, s->n, s->bins_fm, s->n_stride, s->leaf, nullptr, s->ts, st);
-            launch_leafsum(D, s->n, s->leaf, s->wd1, s->weight, s->ts, s->leaf_sums, st);
-            launches += 2;
+            launch_route_leafsum(l, s->n, s->bins_fm, s->n_stride, s->leaf, s->wd1, s->weight, s->ts,
+                                 s->leaf_sums, st);
+            launches += 1;
             rec(e + 4);
             int rc = allreduce(s, s->leaf_sums, (size_t)2 * L, ncclUint64, ncclSum);
             if (rc) return rc;
