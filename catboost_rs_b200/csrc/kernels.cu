@@ -481,47 +481,51 @@ __device__ __forceinline__ double der1_of(int loss, double a, double t, double q
     return __dsub_rn(t, p);
 }
 
-// Eight consecutive doubles from p + i0 (64-byte aligned when the run is
+// kDerHalf consecutive doubles from p + i (32-byte aligned when the half is
 // full), `fill` past n.
-__device__ __forceinline__ void load_run(const double* __restrict__ p, int64_t i0, int64_t n, bool full, double fill,
-                                         double (&v)[kBootRun]) {
+constexpr int kDerHalf = kBootRun / 2;  // rows a thread carries through the derivative math at once
+
+__device__ __forceinline__ void load_half(const double* __restrict__ p, int64_t i, int64_t n, bool full, double fill,
+                                          double (&v)[kDerHalf]) {
     if (full) {
 #pragma unroll
-        for (int k = 0; k < kBootRun; k += 2) {
-            const double2 x = *(const double2*)(p + i0 + k);
+        for (int k = 0; k < kDerHalf; k += 2) {
+            const double2 x = *(const double2*)(p + i + k);
             v[k] = x.x;
             v[k + 1] = x.y;
         }
     } else {
 #pragma unroll
-        for (int k = 0; k < kBootRun; ++k) v[k] = i0 + k < n ? p[i0 + k] : fill;
+        for (int k = 0; k < kDerHalf; ++k) v[k] = i + k < n ? p[i + k] : fill;
     }
 }
 
-__device__ __forceinline__ void store_run(double* __restrict__ p, int64_t i0, int64_t n, bool full,
-                                          const double (&v)[kBootRun]) {
+__device__ __forceinline__ void store_half(double* __restrict__ p, int64_t i, int64_t n, bool full,
+                                           const double (&v)[kDerHalf]) {
     if (full) {
 #pragma unroll
-        for (int k = 0; k < kBootRun; k += 2) *(double2*)(p + i0 + k) = make_double2(v[k], v[k + 1]);
+        for (int k = 0; k < kDerHalf; k += 2) *(double2*)(p + i + k) = make_double2(v[k], v[k + 1]);
     } else {
 #pragma unroll
-        for (int k = 0; k < kBootRun; ++k)
-            if (i0 + k < n) p[i0 + k] = v[k];
+        for (int k = 0; k < kDerHalf; ++k)
+            if (i + k < n) p[i + k] = v[k];
     }
 }
 
 // Each thread takes runs of kBootRun consecutive rows.  kBoot 1 / 2 draws the
 // run's Bayesian / Bernoulli sample here (boot_run, one RNG jump per run) and
 // stores it to sw32 as the bootstrap kernel would; otherwise the sample is
-// read as s_mode says (unless deferred to MVS).  kWeight: per-row weights.
+// read as s_mode says (unless deferred to MVS).  The derivative math then
+// runs over the run's two halves in turn (fewer live registers, more warps
+// per SM).  kWeight: per-row weights.
 template <bool kWeight, int kBoot>
-__global__ void __launch_bounds__(256, 2) der_kernel(
+__global__ void __launch_bounds__(256, 3) der_kernel(
     int64_t n, int loss, double* __restrict__ approx, const double* __restrict__ target,
     const double* __restrict__ weight, const uint16_t* __restrict__ leaf,
     const double* __restrict__ lrv_in, const TreeParams* __restrict__ tp, int s_mode, float* __restrict__ sw32,
     const double* __restrict__ sw64, double* __restrict__ wd1, TreeState* ts, bool defer,
     int64_t row_offset, double rate, float temp, const ull* __restrict__ jump) {
-    static_assert(kBootRun == 8, "a run is one 16-byte load of leaf ids");
+    static_assert(kBootRun == 8, "a run's leaf ids are one 16-byte load");
     const double* lrv = tp->pending ? lrv_in : nullptr;
     const double qa = tp->q_alpha, qd = tp->q_delta;
     double m[4] = {0.0, 0.0, 0.0, 0.0};
@@ -531,66 +535,73 @@ __global__ void __launch_bounds__(256, 2) der_kernel(
          run += (int64_t)gridDim.x * blockDim.x) {
         const int64_t i0 = run * kBootRun;
         const bool full = i0 + kBootRun <= n;
-        double a[kBootRun], t[kBootRun], w[kBootRun], sv[kBootRun];
-        load_run(approx, i0, n, full, 0.0, a);
+        float sv32[kBootRun];
+        if (kBoot) {
+            boot_run(kBoot, i0, row_offset + i0, n, tp, rate, temp, jump, sv32);
+            if (full) {
+                ((float4*)(sw32 + i0))[0] = make_float4(sv32[0], sv32[1], sv32[2], sv32[3]);
+                ((float4*)(sw32 + i0))[1] = make_float4(sv32[4], sv32[5], sv32[6], sv32[7]);
+            } else {
+                for (int k = 0; i0 + k < n; ++k) sw32[i0 + k] = sv32[k];
+            }
+        }
+        uint32_t pw[4] = {0u, 0u, 0u, 0u};  // the run's leaf ids, two per word
         if (lrv) {
-            uint32_t id[kBootRun];
             if (full) {
                 const uint4 p = *(const uint4*)(leaf + i0);
-                const uint32_t pw[4] = {p.x, p.y, p.z, p.w};
-#pragma unroll
-                for (int k = 0; k < kBootRun; ++k) id[k] = (pw[k >> 1] >> ((k & 1) * 16)) & 0xffffu;
+                pw[0] = p.x; pw[1] = p.y; pw[2] = p.z; pw[3] = p.w;
+            } else {
+                for (int k = 0; i0 + k < n; ++k) pw[k >> 1] |= (uint32_t)leaf[i0 + k] << ((k & 1) * 16);
+            }
+        }
+#pragma unroll 1
+        for (int h = 0; h < 2; ++h) {
+            const int64_t i = i0 + h * kDerHalf;
+            double a[kDerHalf], t[kDerHalf], w[kDerHalf], sv[kDerHalf], wd[kDerHalf];
+            load_half(approx, i, n, full, 0.0, a);
+            load_half(target, i, n, full, 0.0, t);
+            if (kWeight) {
+                load_half(weight, i, n, full, 1.0, w);
             } else {
 #pragma unroll
-                for (int k = 0; k < kBootRun; ++k) id[k] = i0 + k < n ? leaf[i0 + k] : 0u;
+                for (int k = 0; k < kDerHalf; ++k) w[k] = 1.0;
             }
+            if (lrv) {
+                const uint32_t hw[2] = {h ? pw[2] : pw[0], h ? pw[3] : pw[1]};  // this half's ids
 #pragma unroll
-            for (int k = 0; k < kBootRun; ++k)
-                if (i0 + k < n) a[k] = __dadd_rn(a[k], __ldg(lrv + id[k]));
-            store_run(approx, i0, n, full, a);
-        }
-        load_run(target, i0, n, full, 0.0, t);
-        if (kWeight) {
-            load_run(weight, i0, n, full, 1.0, w);
-        } else {
+                for (int k = 0; k < kDerHalf; ++k) {
+                    const uint32_t id = (hw[k >> 1] >> ((k & 1) * 16)) & 0xffffu;
+                    if (i + k < n) a[k] = __dadd_rn(a[k], __ldg(lrv + id));
+                }
+                store_half(approx, i, n, full, a);
+            }
+            if (kBoot) {
 #pragma unroll
-            for (int k = 0; k < kBootRun; ++k) w[k] = 1.0;
-        }
-        if (kBoot) {
-            float v[kBootRun];
-            boot_run(kBoot, i0, row_offset + i0, n, tp, rate, temp, jump, v);
-            if (full) {
-                ((float4*)(sw32 + i0))[0] = make_float4(v[0], v[1], v[2], v[3]);
-                ((float4*)(sw32 + i0))[1] = make_float4(v[4], v[5], v[6], v[7]);
+                for (int k = 0; k < kDerHalf; ++k) sv[k] = (double)(h ? sv32[kDerHalf + k] : sv32[k]);
+            } else if (!defer && s_mode == 2) {
+                load_half(sw64, i, n, full, 1.0, sv);
             } else {
-                for (int k = 0; i0 + k < n; ++k) sw32[i0 + k] = v[k];
+#pragma unroll
+                for (int k = 0; k < kDerHalf; ++k)
+                    sv[k] = (!defer && s_mode == 1 && i + k < n) ? (double)sw32[i + k] : 1.0;
             }
 #pragma unroll
-            for (int k = 0; k < kBootRun; ++k) sv[k] = (double)v[k];
-        } else if (!defer && s_mode == 2) {
-            load_run(sw64, i0, n, full, 1.0, sv);
-        } else {
-#pragma unroll
-            for (int k = 0; k < kBootRun; ++k)
-                sv[k] = (!defer && s_mode == 1 && i0 + k < n) ? (double)sw32[i0 + k] : 1.0;
-        }
-        double wd[kBootRun];
-#pragma unroll
-        for (int k = 0; k < kBootRun; ++k) {
-            wd[k] = 0.0;
-            if (i0 + k >= n) continue;
-            wd[k] = __dmul_rn(der1_of(loss, a[k], t[k], qa, qd), w[k]);
-            m[2] = fmax(m[2], fabs(wd[k]));
-            m[3] = fmax(m[3], fabs(w[k]));
-            bad |= !isfinite(wd[k]);
-            if (!defer) {
-                const double g = __dmul_rn(wd[k], sv[k]), h = __dmul_rn(w[k], sv[k]);
-                m[0] = fmax(m[0], fabs(g));
-                m[1] = fmax(m[1], fabs(h));
-                bad |= !isfinite(g) || !isfinite(h);
+            for (int k = 0; k < kDerHalf; ++k) {
+                wd[k] = 0.0;
+                if (i + k >= n) continue;
+                wd[k] = __dmul_rn(der1_of(loss, a[k], t[k], qa, qd), w[k]);
+                m[2] = fmax(m[2], fabs(wd[k]));
+                m[3] = fmax(m[3], fabs(w[k]));
+                bad |= !isfinite(wd[k]);
+                if (!defer) {
+                    const double g = __dmul_rn(wd[k], sv[k]), hh = __dmul_rn(w[k], sv[k]);
+                    m[0] = fmax(m[0], fabs(g));
+                    m[1] = fmax(m[1], fabs(hh));
+                    bad |= !isfinite(g) || !isfinite(hh);
+                }
             }
+            store_half(wd1, i, n, full, wd);
         }
-        store_run(wd1, i0, n, full, wd);
     }
     if (bad) atomicOr(&ts->err, kErrOverflow);
     block_max4(m, ts);
@@ -647,22 +658,21 @@ void launch_max_gh(int64_t n, const double* wd1, const double* weight, const flo
 // row value splits into hi = v >> 17 (|hi| <= 2^16) and lo = v & (2^17 - 1) whose
 // 32-bit sums over a kChunkRows-row work item cannot overflow; resolution is
 // 2^-33 of the largest value.  Leaf channels: max|v| * n_total * 2^s < 2^62.
-__global__ void scales_kernel(TreeState* ts, int64_t n_total, int64_t n_local) {
-    if (threadIdx.x != 0) return;
-    ts->hist_rows[0] = (uint32_t)n_local;  // level 0 histograms every row
-    for (int c = 0; c < 4; ++c) {
-        const double m = __longlong_as_double((long long)ts->maxbits[c]);
-        // score channels: max |v| * 2^s < 2^kPackBits; leaf channels: any sum
-        // over n_total rows stays below 2^62
-        const int s = c < 2 ? fixed_shift(m, kPackBits)
-                            : fixed_shift(__dmul_rn(m, (double)(n_total > 0 ? n_total : 1)), 62);
-        ts->sc.scale[c] = pow2_of(s);
-        ts->sc.inv[c] = pow2_of(-s);
-    }
+// The fixed-point exponent of channel c from the tree's maxima.
+__device__ __forceinline__ int channel_shift(const TreeState* ts, int c, int64_t n_total) {
+    const double m = __longlong_as_double((long long)ts->maxbits[c]);
+    // score channels: max |v| * 2^s < 2^kPackBits; leaf channels: any sum
+    // over n_total rows stays below 2^62
+    return c < 2 ? fixed_shift(m, kPackBits) : fixed_shift(__dmul_rn(m, (double)(n_total > 0 ? n_total : 1)), 62);
 }
 
-void launch_scales(TreeState* ts, int64_t n_total, int64_t n_local, cudaStream_t st) {
-    scales_kernel<<<1, 32, 0, st>>>(ts, n_total, n_local);
+__device__ __forceinline__ void write_scales(TreeState* ts, int64_t n_total, int64_t n_local) {
+    ts->hist_rows[0] = (uint32_t)n_local;  // level 0 histograms every row
+    for (int c = 0; c < 4; ++c) {
+        const int sh = channel_shift(ts, c, n_total);
+        ts->sc.scale[c] = pow2_of(sh);
+        ts->sc.inv[c] = pow2_of(-sh);
+    }
 }
 
 // Per row: g = wd1 * s, h = w * s (the CPU's score channels, boosting.rs:7700-7732),
@@ -672,10 +682,12 @@ void launch_scales(TreeState* ts, int64_t n_total, int64_t n_local, cudaStream_t
 __global__ void __launch_bounds__(256) pack_stats_kernel(int64_t n, const double* __restrict__ wd1,
                                                          const double* __restrict__ weight, int s_mode,
                                                          const float* __restrict__ sw32,
-                                                         const double* __restrict__ sw64,
-                                                         const TreeState* __restrict__ ts,
-                                                         uint4* __restrict__ qstats) {
-    const Pow2 sg = ts->sc.scale[0], sh = ts->sc.scale[1];
+                                                         const double* __restrict__ sw64, TreeState* ts,
+                                                         int64_t n_total, uint4* __restrict__ qstats) {
+    // every block derives the score channels' scales from the tree's maxima;
+    // block 0 also records all four for the later kernels
+    if (blockIdx.x == 0 && threadIdx.x == 0) write_scales(ts, n_total, n);
+    const Pow2 sg = pow2_of(channel_shift(ts, 0, n_total)), sh = pow2_of(channel_shift(ts, 1, n_total));
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
          i += (int64_t)gridDim.x * blockDim.x) {
         const double w = weight ? weight[i] : 1.0;
@@ -685,11 +697,11 @@ __global__ void __launch_bounds__(256) pack_stats_kernel(int64_t n, const double
 }
 
 void launch_pack_stats(int64_t n, const double* wd1, const double* weight, int s_mode, const float* sw32,
-                       const double* sw64, const TreeState* ts, uint4* qstats, cudaStream_t st) {
+                       const double* sw64, TreeState* ts, int64_t n_total, uint4* qstats, cudaStream_t st) {
     int64_t blocks = (n + 255) / 256;
     if (blocks > 148 * 8) blocks = 148 * 8;
-    if (blocks < 1) return;
-    pack_stats_kernel<<<(unsigned)blocks, 256, 0, st>>>(n, wd1, weight, s_mode, sw32, sw64, ts, qstats);
+    if (blocks < 1) blocks = 1;
+    pack_stats_kernel<<<(unsigned)blocks, 256, 0, st>>>(n, wd1, weight, s_mode, sw32, sw64, ts, n_total, qstats);
 }
 
 __global__ void apply_kernel(int64_t n, double* __restrict__ approx, const uint16_t* __restrict__ leaf,
@@ -1115,7 +1127,7 @@ void launch_derive_prefix(int level, int32_t Fs, int32_t B, const ull* built, co
 // scoring (score.rs:39-265, histogram.rs:1007-1171) + argmax (tree.rs:355-366)
 // Block (border group g, feature f) scores up to 32 consecutive borders
 // (lane = border, so the (g, h) pairs of a child load as one 512-byte run).
-// The per-child terms avg*swd and avg^2*sw are independent, so the 8 warps
+// The per-child terms avg*swd and avg^2*sw are independent, so the 4 warps
 // compute a piece of kScorePiece children into shared memory; then warp 0 adds
 // them to each border's running sums in the CPU's canonical order (false
 // children 0..Q-1, then true), so the sums round as the CPU's do.  The true
@@ -1123,11 +1135,11 @@ void launch_derive_prefix(int level, int32_t Fs, int32_t B, const ull* built, co
 // block.  The last block to finish reduces the per-group winners in (feature,
 // border) order, which is the CPU's first-wins strict-> scan (no spin wait).
 // ============================================================================
-constexpr int kScoreWarps = 8;
-constexpr int kScorePiece = 64;      // children per piece, kScorePiece / kScoreWarps per warp
+constexpr int kScoreWarps = 4;
+constexpr int kScorePiece = 32;      // children per piece, kScorePiece / kScoreWarps per warp
 constexpr int kScoreTotSmem = 256;   // leaves whose totals are staged in shared memory
 
-__global__ void __launch_bounds__(kScoreWarps * 32, 4) score_kernel(int level, int32_t Fs, int32_t f0, int32_t F,
+__global__ void __launch_bounds__(kScoreWarps * 32, 8) score_kernel(int level, int32_t Fs, int32_t f0, int32_t F,
                                                                     int32_t B, const ull* __restrict__ cur,
                                                                     const int32_t* __restrict__ border_counts,
                                                                     double l2, int score_fn,
@@ -1151,25 +1163,30 @@ __global__ void __launch_bounds__(kScoreWarps * 32, 4) score_kernel(int level, i
     const ulonglong2* rows = (const ulonglong2*)(cur + (size_t)fl * Q * B * 2);  // row q at rows + q * B
     const bool tot_smem = Q <= kScoreTotSmem;
     double num = 0.0, den = 1e-100;
-    if (g * 32 < nb) {
+    if (g * 32 < B - 1) {  // nb <= B - 1: groups past every feature's borders do nothing
+        constexpr int kPer = kScorePiece / kScoreWarps;
+        ulonglong2 v[kPer];
+        // piece c0's values for this warp's children; the first piece's loads
+        // go out together with the totals' staging
+        auto load_piece = [&](int c0, int pc) {
+#pragma unroll
+            for (int k = 0; k < kPer; ++k) {
+                const int cc = warp + k * kScoreWarps;
+                v[k] = make_ulonglong2(0ull, 0ull);
+                if (cc < pc && b < B) {  // every row has B bins: no need to wait for nb
+                    const int ch = c0 + cc;  // canonical child index: side * Q + q
+                    const int q = ch >= Q ? ch - Q : ch;
+                    v[k] = rows[(size_t)q * B + b];
+                }
+            }
+        };
+        load_piece(0, 2 * Q < kScorePiece ? 2 * Q : kScorePiece);
         if (tot_smem) {
             for (int q = threadIdx.x; q < Q; q += blockDim.x) s_tot[q] = rows[(size_t)q * B + B - 1];
             __syncthreads();
         }
         for (int c0 = 0; c0 < 2 * Q; c0 += kScorePiece) {
             const int pc = 2 * Q - c0 < kScorePiece ? 2 * Q - c0 : kScorePiece;
-            constexpr int kPer = kScorePiece / kScoreWarps;
-            ulonglong2 v[kPer];
-#pragma unroll
-            for (int k = 0; k < kPer; ++k) {
-                const int cc = warp + k * kScoreWarps;
-                v[k] = make_ulonglong2(0ull, 0ull);
-                if (cc < pc && in) {
-                    const int ch = c0 + cc;  // canonical child index: side * Q + q
-                    const int q = ch >= Q ? ch - Q : ch;
-                    v[k] = rows[(size_t)q * B + b];
-                }
-            }
 #pragma unroll
             for (int k = 0; k < kPer; ++k) {
                 const int cc = warp + k * kScoreWarps;
@@ -1193,6 +1210,10 @@ __global__ void __launch_bounds__(kScoreWarps * 32, 4) score_kernel(int level, i
                     }
                     s_t[cc][lane] = term;
                 }
+            }
+            if (c0 + kScorePiece < 2 * Q) {  // the next piece's loads overlap the ordered sum
+                const int nc = c0 + kScorePiece;
+                load_piece(nc, 2 * Q - nc < kScorePiece ? 2 * Q - nc : kScorePiece);
             }
             __syncthreads();
             if (warp == 0 && in) {
@@ -1251,15 +1272,32 @@ __global__ void __launch_bounds__(kScoreWarps * 32, 4) score_kernel(int level, i
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    // (feature, border) order: key f * 256 + border, lowest key wins ties
+    // (feature, border) order: key f * 256 + border, lowest key wins ties.
+    // The other blocks' records are read from L2 (ld.cg), a batch of loads
+    // in flight per thread.
     double fb = -INFINITY;
     int fk = 0x7fffffff;
-    for (int e = threadIdx.x; e < Fs * G; e += blockDim.x) {
-        const double sc = ((volatile double*)grp_score)[e];
-        const int bin = ((volatile int32_t*)grp_bin)[e];
-        if (bin == 0x7fffffff) continue;
-        const int key = (f0 + e / G) * 256 + bin;
-        if (better(sc, key, fb, fk)) { fb = sc; fk = key; }
+    constexpr int kBatch = 8;
+    for (int e0 = threadIdx.x; e0 < Fs * G; e0 += blockDim.x * kBatch) {
+        double sc[kBatch];
+        int bin[kBatch];
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+            const int e = e0 + j * blockDim.x;
+            sc[j] = -INFINITY;
+            bin[j] = 0x7fffffff;
+            if (e < Fs * G) {
+                sc[j] = __ldcg(grp_score + e);
+                bin[j] = __ldcg(grp_bin + e);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+            const int e = e0 + j * blockDim.x;
+            if (bin[j] == 0x7fffffff) continue;
+            const int key = (f0 + e / G) * 256 + bin[j];
+            if (better(sc[j], key, fb, fk)) { fb = sc[j]; fk = key; }
+        }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
@@ -1469,7 +1507,7 @@ __device__ __forceinline__ void route_rows(int level, int64_t n, int64_t r0, con
 // global slot per row.  The block then reserves one range per parent and
 // writes its rows there.
 template <int kQ>
-__global__ void __launch_bounds__(kRouteThreads, 4) partition_kernel(int level, int64_t n,
+__global__ void __launch_bounds__(kRouteThreads, 6) partition_kernel(int level, int64_t n,
                                                                      const uint8_t* __restrict__ bins_fm,
                                                                      int64_t n_stride,
                                                                      const TreeState* __restrict__ ts,
@@ -1505,12 +1543,23 @@ __global__ void __launch_bounds__(kRouteThreads, 4) partition_kernel(int level, 
     // per row: parent << 16 | rank among the warp's rows of that parent (a
     // warp has 512 rows), or ~0 when the row is not listed
     uint32_t pr[kRouteRows];
+    if (Q <= 64) {  // build sides as a bit mask in registers
+        const unsigned long long sides =
+            (unsigned long long)__ballot_sync(kFull, (uint32_t)lane < Q && s_side[lane]) |
+            (Q > 32 ? (unsigned long long)__ballot_sync(kFull, (uint32_t)lane + 32 < Q && s_side[lane + 32]) << 32
+                    : 0ull);
 #pragma unroll
-    for (int k = 0; k < kRouteRows; ++k) {
-        pr[k] = 0xffffffffu;
-        if (lv[k] != 0xffffffffu) {
+        for (int k = 0; k < kRouteRows; ++k) {
             const uint32_t q = lv[k] & (Q - 1u);
-            if ((lv[k] >> level) == (uint32_t)s_side[q]) pr[k] = q << 16;
+            const bool sel = lv[k] != 0xffffffffu && (lv[k] >> level) == (uint32_t)(sides >> q & 1ull);
+            pr[k] = sel ? q << 16 : 0xffffffffu;
+        }
+    } else {
+#pragma unroll
+        for (int k = 0; k < kRouteRows; ++k) {
+            const uint32_t q = lv[k] & (Q - 1u);
+            const bool sel = lv[k] != 0xffffffffu && (lv[k] >> level) == (uint32_t)s_side[q];
+            pr[k] = sel ? q << 16 : 0xffffffffu;
         }
     }
     if (kQ > 0) {
@@ -1563,6 +1612,8 @@ __global__ void __launch_bounds__(kRouteThreads, 4) partition_kernel(int level, 
 // is not null, the 2Q children's row counts (child q + side * Q) with their
 // segments (exclusive prefix in child order) as rows_out / base_out, and
 // cursor_out = base_out for the next partition.
+constexpr uint32_t kSegItemSmem = 2048;  // parents whose work items all threads write
+
 __global__ void __launch_bounds__(1024) segments_kernel(int level, int64_t n, const uint32_t* __restrict__ rows_in,
                                                         const uint32_t* __restrict__ base_in,
                                                         const uint32_t* __restrict__ cursor,
@@ -1571,6 +1622,7 @@ __global__ void __launch_bounds__(1024) segments_kernel(int level, int64_t n, co
                                                         uint32_t* __restrict__ cursor_out, HistChunk* __restrict__ chunks,
                                                         uint32_t cap, uint32_t* __restrict__ n_chunks, TreeState* ts) {
     __shared__ uint32_t s_scan[40];
+    __shared__ uint32_t s_first[kSegItemSmem];  // first work item of each parent
     const uint32_t Q = 1u << level;
     const uint32_t per = (Q + blockDim.x - 1) / blockDim.x;
     const uint32_t q0 = threadIdx.x * per;
@@ -1585,11 +1637,32 @@ __global__ void __launch_bounds__(1024) segments_kernel(int level, int64_t n, co
     uint32_t rows_tot, items_tot;
     (void)block_excl_scan<uint32_t>(rows, s_scan, &rows_tot);
     uint32_t item = block_excl_scan<uint32_t>(items, s_scan, &items_tot);
-    for (uint32_t q = q0; q < q0 + per && q < Q; ++q) {
-        const uint32_t b = base_of(q), cnt = cursor[q] - b;
-        for (uint32_t st = 0; st < cnt; st += cr) {
-            if (item < cap) chunks[item] = HistChunk{q, b + st, cnt - st < cr ? cnt - st : cr, 0u};
-            ++item;
+    if (Q <= kSegItemSmem) {
+        // few parents, many items each: every thread writes items, finding
+        // an item's parent by binary search over the parents' first items
+        for (uint32_t q = q0; q < q0 + per && q < Q; ++q) {
+            s_first[q] = item;
+            item += (cursor[q] - base_of(q) + cr - 1) / cr;
+        }
+        __syncthreads();
+        const uint32_t lim = items_tot < cap ? items_tot : cap;
+        for (uint32_t it = threadIdx.x; it < lim; it += blockDim.x) {
+            uint32_t lo = 0, hi = Q - 1;  // last parent whose first item <= it
+            while (lo < hi) {
+                const uint32_t mid = (lo + hi + 1) >> 1;
+                if (s_first[mid] <= it) lo = mid;
+                else hi = mid - 1;
+            }
+            const uint32_t b = base_of(lo), cnt = cursor[lo] - b, st = (it - s_first[lo]) * cr;
+            chunks[it] = HistChunk{lo, b + st, cnt - st < cr ? cnt - st : cr, 0u};
+        }
+    } else {
+        for (uint32_t q = q0; q < q0 + per && q < Q; ++q) {
+            const uint32_t b = base_of(q), cnt = cursor[q] - b;
+            for (uint32_t st = 0; st < cnt; st += cr) {
+                if (item < cap) chunks[item] = HistChunk{q, b + st, cnt - st < cr ? cnt - st : cr, 0u};
+                ++item;
+            }
         }
     }
     if (threadIdx.x == 0) {

@@ -224,10 +224,11 @@ void launch_der(int64_t n, int loss, double* approx, const double* target, const
                 double rate, float temp, const ull* jump, cudaStream_t st);
 void launch_max_gh(int64_t n, const double* wd1, const double* weight, const float* sw32, TreeState* ts,
                    cudaStream_t st);
-// also records this rank's level-0 row count in ts->hist_rows[0]
-void launch_scales(TreeState* ts, int64_t n_total, int64_t n_local, cudaStream_t st);
+// Packs every row's score channels; derives the fixed-point scales of all
+// four channels from the tree's maxima itself and records them in ts->sc for
+// the later kernels, with this rank's level-0 row count in ts->hist_rows[0].
 void launch_pack_stats(int64_t n, const double* wd1, const double* weight, int s_mode, const float* sw32,
-                       const double* sw64, const TreeState* ts, uint4* qstats, cudaStream_t st);
+                       const double* sw64, TreeState* ts, int64_t n_total, uint4* qstats, cudaStream_t st);
 void launch_apply(int64_t n, double* approx, const uint16_t* leaf, const double* lrv,
                   cudaStream_t st);
 

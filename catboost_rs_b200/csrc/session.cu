@@ -590,9 +590,8 @@ int enqueue_tree(cbgpu_session* s, int set, bool prof, int boot_mode, int s_mode
         int rc = allreduce(s, maxbits, 4, ncclUint64, ncclMax);
         if (rc) return rc;
     }
-    launch_scales(s->ts, s->n_total, s->n, st);
-    launch_pack_stats(s->n, s->wd1, s->weight, s_mode, s->sw32, s->sw64, s->ts, s->qstats, st);
-    launches += 2;
+    launch_pack_stats(s->n, s->wd1, s->weight, s_mode, s->sw32, s->sw64, s->ts, s->n_total, s->qstats, st);
+    launches += 1;
     rec(1);
 
     // ---- level loop
