@@ -4,7 +4,7 @@
  * This library replaces the device half of catboost_rs's compute seam: the
  * `cb_compute::Runtime` trait methods that `cb_train`'s boosting loop calls
  * (crates/cb-compute/src/runtime.rs:1410-1651).  A thin Rust shim implements
- * `Runtime` on top of these entry points (see INTEGRATION.md); everything
+ * `Runtime` on top of these entry points; everything
  * above the seam (cb-train's loop, cb-data's pool, the fit/predict APIs)
  * stays unchanged.
  *
