@@ -15,3 +15,5 @@ from .boosting import (FitParams, MultiClassModel, ObliviousModel, RankingModel,
 __version__ = "0.1.0"
 from . import model_json  # noqa: F401,E402
 from .model_json import from_json, load_json, save_json, to_json  # noqa: F401,E402
+from . import model_cbm  # noqa: F401,E402
+from .model_cbm import load_cbm, save_cbm  # noqa: F401,E402

@@ -425,6 +425,33 @@ def model_json_fixtures(ref):
     return ["model_json/" + k for k in docs]
 
 
+def cbm_fixtures(ref):
+    """Upstream .cbm model files (the reference's binary model format,
+    crates/cb-model/src/cbm.rs) as raw bytes, with what pins them: the same
+    model's model.json where upstream wrote one, and upstream's predictions
+    on the fixture rows (model_sum).  The one-hot fits' rows, categories and
+    predictions are in one_hot.npz."""
+    fx = os.path.join(ref, "crates/cb-oracle/fixtures")
+    files = {"model_sum_m0": ("model_sum/m0.cbm", None), "model_sum_m1": ("model_sum/m1.cbm", None),
+             "mae": ("fstr_loss_change/mae_model.cbm", "fstr_loss_change/mae_model.json"),
+             "partial_dependence": ("partial_dependence/model.cbm", "partial_dependence/model.json"),
+             "staged_predict": ("staged_predict/model.cbm", None),
+             "one_hot_default_binary": ("one_hot_train/default_binary/model.cbm",
+                                        "one_hot_train/default_binary/model.json"),
+             "one_hot_multi": ("one_hot_train/multi/model.cbm", "one_hot_train/multi/model.json")}
+    arrays = {}
+    for name, (cbm, js) in files.items():
+        with open(os.path.join(fx, cbm), "rb") as f:
+            arrays[name + "__cbm"] = np.frombuffer(f.read(), dtype=np.uint8)
+        if js:
+            arrays[name + "__json"] = np.array(json.dumps(json.loads(_read(os.path.join(fx, js)))))
+    arrays["model_sum__X"] = np.load(os.path.join(fx, "model_sum/X.npy")).astype(np.float32)
+    for m in ("m0", "m1"):
+        arrays[f"model_sum__expected_{m}"] = np.load(os.path.join(fx, f"model_sum/expected_{m}.npy")).astype(np.float64)
+    np.savez_compressed(os.path.join(OUT, "model_cbm.npz"), **arrays)
+    return ["model_cbm/" + k for k in files]
+
+
 def main():
     ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("CB_REFERENCE", "")
     if not ref or not os.path.isdir(ref):
@@ -438,6 +465,7 @@ def main():
     written += ranking_fixtures(ref)
     written += one_hot_fixtures(ref)
     written += model_json_fixtures(ref)
+    written += cbm_fixtures(ref)
     with open(os.path.join(OUT, "MANIFEST.json"), "w") as f:
         json.dump({"generator": "tests/golden/make_golden.py",
                    "origin": "upstream CatBoost 1.2.10 fixtures committed under the reference's "
