@@ -5,6 +5,7 @@ depth 8, lr 0.05, Bayesian bootstrap T=1, Cosine score, l2 3), plus the
 histogram kernel's achieved HBM bandwidth against the measured peak.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py --config 3|4 [--variant ...]   (bench_configs.py: MultiClass / ranking)
 
 A step is one boosting iteration (one tree).  Multi-GPU runs are launched by
 torchrun, one rank per GPU; rows are document-sharded (strong scaling: the
@@ -85,27 +86,56 @@ def _block(b: int, F: int, seed: int):
     return X, y
 
 
-def make_shard(row_offset: int, n: int, F: int, seed: int):
+def make_shard(row_offset: int, n: int, F: int, seed: int, block=None):
     """Rows [row_offset, row_offset + n) as features [F][n] f32 and labels; the
     1Mi-row blocks are generated on a thread pool (each block has its own
-    seeded generator, so the rows do not depend on the thread count)."""
+    seeded generator, so the rows do not depend on the thread count).  block:
+    the per-block generator (config 2's by default)."""
+    block = block or _block
     from concurrent.futures import ThreadPoolExecutor
     X = np.empty((F, n), dtype=np.float32)
     y = np.empty(n, dtype=np.float64)
     b0, b1 = row_offset // BLOCK_ROWS, (row_offset + n - 1) // BLOCK_ROWS
 
     def fill(b):
-        Xb, yb = _block(b, F, seed)
+        Xb, yb = block(b, F, seed)
         lo = max(row_offset, b * BLOCK_ROWS)
         hi = min(row_offset + n, (b + 1) * BLOCK_ROWS)
         X[:, lo - row_offset:hi - row_offset] = Xb[:, lo - b * BLOCK_ROWS:hi - b * BLOCK_ROWS]
         y[lo - row_offset:hi - row_offset] = yb[lo - b * BLOCK_ROWS:hi - b * BLOCK_ROWS]
 
     if n > 0:
-        workers = max(1, min(b1 - b0 + 1, os.cpu_count() or 1, 16))
+        # each worker holds one F x 1Mi block: share the host cores among the
+        # ranks of a box so their blocks fit in host memory together
+        per_rank = max(1, (os.cpu_count() or 1) // max(1, int(os.environ.get("LOCAL_WORLD_SIZE", "1"))))
+        workers = max(1, min(b1 - b0 + 1, per_rank, 16))
         with ThreadPoolExecutor(workers) as ex:
             list(ex.map(fill, range(b0, b1 + 1)))
     return X, y
+
+
+def _block5(b: int, F: int, seed: int):
+    """Config 5 rows: F N(0,1) f32 features, target = a sparse linear score over
+    25 features plus N(0, 0.1) noise (RMSE)."""
+    g = np.random.default_rng([seed, b, 5])
+    X = g.standard_normal((F, BLOCK_ROWS), dtype=np.float32)
+    gw = np.random.default_rng([seed, 1 << 30, 5])
+    k = min(25, F)
+    feats = gw.choice(F, size=k, replace=False)
+    y = gw.standard_normal(k) @ X[feats].astype(np.float64) + 0.1 * g.standard_normal(BLOCK_ROWS)
+    return X, y
+
+
+def make_borders5(F: int, border_count: int, seed: int):
+    """Uniform-quantile borders of config 5's N(0,1) features from a fixed-seed
+    200k sample (no NaN, so no sentinel)."""
+    g = np.random.default_rng([seed, 1 << 31, 5])
+    out = []
+    for _ in range(F):
+        s = g.standard_normal(BORDER_SAMPLE).astype(np.float32).astype(np.float64)
+        q = np.quantile(s, np.linspace(0, 1, border_count + 1)[1:-1])
+        out.append(np.unique(q.astype(np.float32).astype(np.float64)))
+    return out
 
 
 def make_borders(F: int, border_count: int, seed: int):
@@ -249,12 +279,13 @@ def cpu_reference_run(args, X, y, trees: int, warm: int, budget_s: float):
     `warm` untimed trees first; then `trees` timed trees, fewer when the
     warm-up tree's time says they would exceed `budget_s` (at least 3)."""
     from oracle import oracle as orc
-    borders = make_borders(args.features, args.border_count, args.seed)
+    c5 = getattr(args, "config", 2) == 5
+    borders = (make_borders5 if c5 else make_borders)(args.features, args.border_count, args.seed)
     bins = orc.quantize(X, borders)
     threads = os.cpu_count() or 1
-    kw = dict(loss="Logloss", depth=args.depth, learning_rate=0.05, l2_leaf_reg=3.0,
-              score_function="Cosine", bootstrap_type="Bayesian", bagging_temperature=1.0,
-              random_seed=0, boost_from_average=False, staged=False, n_threads=threads)
+    kw = dict(loss="RMSE" if c5 else "Logloss", depth=args.depth, learning_rate=0.05, l2_leaf_reg=3.0,
+              score_function="Cosine", bootstrap_type="MVS" if c5 else "Bayesian", bagging_temperature=1.0,
+              subsample=0.8, random_seed=0, boost_from_average=False, staged=False, n_threads=threads)
     counts = [len(b) for b in borders]
     if warm:
         t0 = time.perf_counter()
@@ -286,25 +317,45 @@ def main():
     ap.add_argument("--cpu-budget-s", type=float, default=60.0)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4, 5],
+                    help="BASELINE config: 2 (default) or 5 (RMSE 50M x 500, depth 10, MVS) on this file's "
+                         "scalar session; 3 (MultiClass) or 4 (ranking) from bench_configs.py")
+    ap.add_argument("--variant", default=None, help="config 3: onehot | bernoulli; config 4: yetirank | pairlogit")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.config == 5:  # its shape unless overridden on the command line
+        for k, v in (("rows", 50_000_000), ("features", 500), ("depth", 10)):
+            if getattr(args, k) == ap.get_default(k):
+                setattr(args, k, v)
+    if args.config in (3, 4):
+        import bench_configs
+        if args.seed == 20261201:
+            args.seed = 0
+        (bench_configs.run_config3 if args.config == 3 else bench_configs.run_config4)(args)
+        return
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-    metric = "trees/sec at 10M x 200 depth-8 Logloss"
-    base_cfg = {"workload": "config2: Logloss 10M x 200 f32 (half N(0,1), half U(0,1), 5% NaN), "
+    c5 = args.config == 5
+    metric = "trees/sec at 50M x 500 depth-10 RMSE (MVS)" if c5 else "trees/sec at 10M x 200 depth-8 Logloss"
+    loss, boot = ("RMSE", "MVS") if c5 else ("Logloss", "Bayesian")
+    block = _block5 if c5 else _block
+    base_cfg = {"workload": "config5: RMSE 50M x 500 N(0,1) f32, sparse linear target + noise, border_count 128, "
+                            "depth 10, lr 0.05, MVS subsample 0.8, Cosine, l2 3" if c5 else
+                            "config2: Logloss 10M x 200 f32 (half N(0,1), half U(0,1), 5% NaN), "
                             "border_count 128 (nan_mode Min), depth 8, lr 0.05, Bayesian T=1, Cosine, l2 3",
                 "rows": args.rows, "features": args.features, "depth": args.depth,
                 "border_count": args.border_count, "parallelism": f"doc-shard x{world}",
-                "l2_flush": "inputs larger than L2 (2.2 GB of row-major bins re-read per tree)"}
+                "l2_flush": "inputs larger than L2 (%.1f GB of row-major bins re-read per tree)"
+                            % (args.rows * -(-args.features // 32) * 32 / 1e9)}
 
     if args.impl == "reference":
         if rank != 0:
             return
         # the full workload (every row and feature); the timed trees are bounded
         # by a time budget so the run ends within a few minutes
-        X, y = make_shard(0, args.rows, args.features, args.seed)
+        X, y = make_shard(0, args.rows, args.features, args.seed, block)
         tps, cores, dt, timed = cpu_reference_run(args, X, y, args.steps, 1, 2.0 * args.cpu_budget_s)
         sample = (f"C restatement of the reference CPU path (oracle/), full workload {args.rows} rows x "
                   f"{args.features} features at depth {args.depth}, {cores} threads: 1 warm-up tree, then "
@@ -332,8 +383,8 @@ def main():
 
     F = args.features
     row_offset, n = shard_bounds(args.rows, world, rank)
-    X, y = make_shard(row_offset, n, F, args.seed)
-    borders = make_borders(F, args.border_count, args.seed)
+    X, y = make_shard(row_offset, n, F, args.seed, block)
+    borders = (make_borders5 if c5 else make_borders)(F, args.border_count, args.seed)
     cols = [X[f] for f in range(F)]
     def fresh_uid():
         # an NCCL unique id serves one communicator: every session gets its own
@@ -346,11 +397,11 @@ def main():
     def open_session(sample_from_host: bool):
         uid = fresh_uid()
         rt = cb.B200Runtime()
-        cfg = cb.DeviceTrainConfig(bootstrap_type="Bayesian", bagging_temperature=1.0, rng_seed=0, bias=0.0,
-                                   sample_from_host=sample_from_host, device=local_rank, rank=rank,
+        cfg = cb.DeviceTrainConfig(bootstrap_type=boot, bagging_temperature=1.0, sample_rate=0.8, rng_seed=0,
+                                   bias=0.0, sample_from_host=sample_from_host, device=local_rank, rank=rank,
                                    world_size=world, row_offset=row_offset, n_total=args.rows,
                                    nccl_unique_id=uid)
-        ok = rt.begin_device_training_raw("Logloss", args.depth, True, 1, "Cosine", cols, borders, None, n, F,
+        ok = rt.begin_device_training_raw(loss, args.depth, True, 1, "Cosine", cols, borders, None, n, F,
                                           max(len(b) for b in borders) + 1, LR_SEAM, 3.0, cfg)
         if not ok:
             raise RuntimeError(rt.decline_reason)
@@ -450,7 +501,7 @@ def main():
         line = {"metric": metric, "value": value, "unit": "trees/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": elapsed / args.steps, "higher_is_better": True,
                 "scaling": "strong", "vs_baseline": None, "dtype": "int64",
-                "data": "synthetic (seeded, config-2 shapes and distributions)", "config": base_cfg,
+                "data": "synthetic (seeded, config-%d shapes and distributions)" % args.config, "config": base_cfg,
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                              "frac": (achieved / peak) if achieved else None,
                              "traffic": (dram_per_row * rows / hist_launches) if dram_per_row else None,
