@@ -1723,14 +1723,6 @@ void launch_segments(int level, int64_t n, const uint32_t* rows_in, const uint32
 constexpr int kLeafSmemDepth = 10;  // deeper trees add into the global sums per row
 constexpr int kLeafsumBlocksPerSm = 4;
 
-// Exact 64-bit add into a shared (lo, hi) u32 pair: the lo add's wrap carries
-// into hi, so hi * 2^32 + lo is the sum mod 2^64 (the true sum fits an int64).
-__device__ __forceinline__ void add_split64(uint32_t* lo, uint32_t* hi, long long v) {
-    const uint32_t l = (uint32_t)(unsigned long long)v;
-    const uint32_t old = atomicAdd(lo, l);
-    atomicAdd(hi, (uint32_t)(v >> 32) + (old + l < old ? 1u : 0u));
-}
-
 __global__ void __launch_bounds__(kRouteThreads) route_leafsum_kernel(int level, int64_t n,
                                                                       const uint8_t* __restrict__ bins_fm,
                                                                       int64_t n_stride,

@@ -190,6 +190,17 @@ CBGPU_HD uint8_t build_true_side(const unsigned long long* winner_rec, int q) {
     return true_child_built(m[2 * q], m[2 * q + 1]);
 }
 
+#ifdef __CUDACC__
+// Exact 64-bit add into a (lo, hi) pair of 32-bit words (shared memory, where
+// 64-bit atomics are slow): the lo add's wrap carries into hi, so
+// hi * 2^32 + lo is the sum mod 2^64 (exact whenever the true sum fits an int64).
+__device__ __forceinline__ void add_split64(uint32_t* lo, uint32_t* hi, long long v) {
+    const uint32_t l = (uint32_t)(unsigned long long)v;
+    const uint32_t old = atomicAdd(lo, l);
+    atomicAdd(hi, (uint32_t)(v >> 32) + (old + l < old ? 1u : 0u));
+}
+#endif
+
 // cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (kernel, device)
 // and size, thread-safe; returns the cudaError_t of the setting (0 = ok).
 int ensure_dyn_smem(const void* kernel, int bytes);

@@ -236,18 +236,22 @@ __global__ void mc_pack_kernel(int64_t n, int K, const double* __restrict__ wd1,
 
 // Level histogram: block (feature f, channel c, rows [r0, r0 + kMcChunk)) adds
 // q[c][row] into cell (leaf, f, bin, c) of hist[leaves][F][NB][C].  The
-// leaves x bins table sits in shared memory when it fits (smem > 0).
+// leaves x bins table sits in shared memory when it fits (smem > 0), each
+// int64 cell as a (lo, hi) pair of 32-bit words added exactly (add_split64):
+// 64-bit shared atomics run as compare-and-swap loops, several times slower.
 __global__ void __launch_bounds__(kMcThreads)
 mc_hist_kernel(int64_t n, int F, int NB, int C, int leaves, const uint8_t* __restrict__ bins_fm,
                const long long* __restrict__ q, const uint16_t* __restrict__ leaf,
                unsigned long long* __restrict__ hist, int use_smem) {
-    extern __shared__ unsigned long long tab[];
+    extern __shared__ uint32_t tab32[];  // [cells] lo words, then [cells] hi words
     const int f = blockIdx.x, c = blockIdx.y;
     const int64_t r0 = (int64_t)blockIdx.z * kMcChunk;
     const int64_t r1 = r0 + kMcChunk < n ? r0 + kMcChunk : n;
     const int cells = leaves * NB;
+    uint32_t* tlo = tab32;
+    uint32_t* thi = tab32 + cells;
     if (use_smem) {
-        for (int k = threadIdx.x; k < cells; k += blockDim.x) tab[k] = 0ull;
+        for (int k = threadIdx.x; k < 2 * cells; k += blockDim.x) tab32[k] = 0u;
         __syncthreads();
     }
     const uint8_t* col = bins_fm + (size_t)f * (size_t)n;
@@ -258,13 +262,13 @@ mc_hist_kernel(int64_t n, int F, int NB, int C, int leaves, const uint8_t* __res
         if (lf >= leaves || b >= NB) continue;
         const long long v = qc[i];
         if (v == 0) continue;
-        if (use_smem) atomicAdd(&tab[lf * NB + b], (unsigned long long)v);
+        if (use_smem) add_split64(tlo + lf * NB + b, thi + lf * NB + b, v);
         else atomicAdd(&hist[(((size_t)lf * F + f) * NB + b) * C + c], (unsigned long long)v);
     }
     if (use_smem) {
         __syncthreads();
         for (int k = threadIdx.x; k < cells; k += blockDim.x) {
-            const unsigned long long v = tab[k];
+            const unsigned long long v = ((unsigned long long)thi[k] << 32) + tlo[k];
             if (v) {
                 const int lf = k / NB, b = k - lf * NB;
                 atomicAdd(&hist[(((size_t)lf * F + f) * NB + b) * C + c], v);
