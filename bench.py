@@ -457,7 +457,8 @@ def main():
         sample = pin((n,), torch.float64)
         rs = np.random.default_rng(7)
         sample[:] = -np.log(rs.random(n))  # Bayesian-like multipliers; content does not change the cost
-        leaf_of = pin((n,), torch.uint8)
+        lb = 1 if args.depth <= 8 else 2  # leaf id bytes the seam returns
+        leaf_of = pin((n,), torch.uint8 if lb == 1 else torch.int16)
         import ctypes as C
         L = cb.load_library()
         D = args.depth
@@ -469,7 +470,7 @@ def main():
 
         def step():
             rc = L.cbgpu_grow_tree(rt2._s, None, yy.ctypes.data, n, sample.ctypes.data, n, sf.ctypes.data,
-                                   sb.ctypes.data, ns.ctypes.data, lv.ctypes.data, leaf_of.ctypes.data, 1)
+                                   sb.ctypes.data, ns.ctypes.data, lv.ctypes.data, leaf_of.ctypes.data, lb)
             if rc:
                 raise RuntimeError(cb._lib.last_error())
         for _ in range(args.warmup):
@@ -483,9 +484,9 @@ def main():
         barrier()
         rt2.end_device_training()
         e2e = {"value": args.steps / (e_ms / 1e3), "unit": "trees/s", "h2d_bytes_per_step": int(n * 8),
-               "d2h_bytes_per_step": int(n + D * 8 + (1 << D) * 8),
+               "d2h_bytes_per_step": int(lb * n + D * 8 + (1 << D) * 8),
                "path": "cbgpu_grow_tree with a pinned host bootstrap sample (sample_from_host, the cb-train "
-                       "contract) uploaded and u8 leaf ids read back every tree"}
+                       "contract) uploaded and leaf ids (u8, u16 past depth 8) read back every tree"}
 
     # ---- CPU baseline (rank 0, N=1 only) -------------------------------------
     cpu = None
