@@ -448,6 +448,8 @@ def main():
     achieved = alg_bytes / (hist_ms / 1e3) / 1e9 if hist_ms > 0 else None
     peak, peak_kind = peaks()
     dram_per_row, dram_cmd = hist_dram_bytes_per_row()
+    if args.config != 2 or F != 200:  # the capture is of config 2's 200-feature rows
+        dram_per_row = None
 
     # ---- end to end through the C ABI with host buffers (e2e) --------------
     e2e = None
@@ -510,7 +512,7 @@ def main():
                              "traffic_source": (f"ncu dram__bytes_read.sum + dram__bytes_write.sum of the eight "
                                                 f"histogram launches of a 2M-row tree, {dram_per_row} B per "
                                                 f"histogrammed row, scaled by rows per launch: {dram_cmd}")
-                             if dram_per_row else "no capture found",
+                             if dram_per_row else "no capture of this workload's row width",
                              "limiter": "shared-memory reduction issue: 4 exact 32-bit red.shared per "
                                         "(row, feature); LSU pipe 70.6% of peak, top stall mio_throttle "
                                         "(ncu, 2M rows)",
