@@ -1419,16 +1419,36 @@ void launch_select_split(int level, int world, int stride, const ull* all_best, 
 struct PartView {
     const uint8_t* col;
     int32_t bin;
+    bool eq;        // one-hot feature: the row passes on bin == value, else on bin > border
+    bool vec;       // the column rows can be read 16 at a time (16-byte aligned)
 };
+
+__device__ __forceinline__ PartView make_part_view(int32_t feature, int32_t bin, int32_t f_eq,
+                                                   const uint8_t* bins_fm, int64_t n_stride) {
+    PartView v;
+    const int f = feature < 0 ? 0 : feature;
+    v.col = bins_fm + (int64_t)f * n_stride;
+    v.bin = feature < 0 ? 0x7fffffff : bin;
+    v.eq = feature >= f_eq;
+    v.vec = (n_stride & 15) == 0;
+    return v;
+}
 
 __device__ __forceinline__ PartView part_view(const TreeState* ts, int level, const uint8_t* bins_fm,
                                               int64_t n_stride) {
-    SplitRec s = ts->split[level];
-    PartView v;
-    int f = s.feature < 0 ? 0 : s.feature;
-    v.col = bins_fm + (int64_t)f * n_stride;
-    v.bin = s.feature < 0 ? 0x7fffffff : s.bin;
-    return v;
+    const SplitRec s = ts->split[level];
+    return make_part_view(s.feature, s.bin, 0x7fffffff, bins_fm, n_stride);
+}
+
+// The split of `level` from a record array of `stride` 32-bit words per level
+// whose first two words are (feature, bin); features >= f_eq route by equality.
+__device__ __forceinline__ PartView part_view_of(const int32_t* splits, int stride, int f_eq, int level,
+                                                 const uint8_t* bins_fm, int64_t n_stride) {
+    return make_part_view(splits[level * stride], splits[level * stride + 1], f_eq, bins_fm, n_stride);
+}
+
+__device__ __forceinline__ uint32_t passes(const PartView& pv, uint32_t b) {
+    return pv.eq ? (uint32_t)((int32_t)b == pv.bin) : (uint32_t)((int32_t)b > pv.bin);
 }
 
 // ============================================================================
@@ -1465,7 +1485,7 @@ constexpr int kPartSmemParents = 256;  // deeper levels reserve one slot per row
 // get ~0.
 __device__ __forceinline__ void route_rows(int level, int64_t n, int64_t r0, const PartView& pv,
                                            uint16_t* __restrict__ leaf, uint32_t (&lv)[kRouteRows]) {
-    if (r0 + kRouteRows <= n) {
+    if (pv.vec && r0 + kRouteRows <= n) {
         const uint4 v = __ldg((const uint4*)(pv.col + r0));  // n_stride and r0 are multiples of 16
         const uint32_t w[4] = {v.x, v.y, v.z, v.w};
         if (level > 0) {
@@ -1479,7 +1499,7 @@ __device__ __forceinline__ void route_rows(int level, int64_t n, int64_t r0, con
         }
 #pragma unroll
         for (int k = 0; k < kRouteRows; ++k)
-            lv[k] |= (uint32_t)((int32_t)((w[k >> 2] >> ((k & 3) * 8)) & 0xffu) > pv.bin) << level;
+            lv[k] |= passes(pv, (w[k >> 2] >> ((k & 3) * 8)) & 0xffu) << level;
         uint4 o0, o1;
         o0.x = lv[0] | (lv[1] << 16); o0.y = lv[2] | (lv[3] << 16);
         o0.z = lv[4] | (lv[5] << 16); o0.w = lv[6] | (lv[7] << 16);
@@ -1493,7 +1513,7 @@ __device__ __forceinline__ void route_rows(int level, int64_t n, int64_t r0, con
             const int64_t i = r0 + k;
             lv[k] = 0xffffffffu;
             if (i < n) {
-                lv[k] = (level > 0 ? (uint32_t)leaf[i] : 0u) | ((uint32_t)((int32_t)pv.col[i] > pv.bin) << level);
+                lv[k] = (level > 0 ? (uint32_t)leaf[i] : 0u) | (passes(pv, pv.col[i]) << level);
                 leaf[i] = (uint16_t)lv[k];
             }
         }
@@ -1510,7 +1530,8 @@ template <int kQ>
 __global__ void __launch_bounds__(kRouteThreads, 6) partition_kernel(int level, int64_t n,
                                                                      const uint8_t* __restrict__ bins_fm,
                                                                      int64_t n_stride,
-                                                                     const TreeState* __restrict__ ts,
+                                                                     const int32_t* __restrict__ splits,
+                                                                     int split_stride, int f_eq,
                                                                      uint16_t* __restrict__ leaf,
                                                                      const uint8_t* __restrict__ small_side,
                                                                      uint32_t* __restrict__ cursor,
@@ -1526,7 +1547,7 @@ __global__ void __launch_bounds__(kRouteThreads, 6) partition_kernel(int level, 
         for (uint32_t q = threadIdx.x; q < Q; q += blockDim.x) s_side[q] = small_side[q];
         for (uint32_t k = threadIdx.x; k < kWarps * Q; k += blockDim.x) s_w[k >> level][k & (Q - 1u)] = 0u;
     }
-    const PartView pv = part_view(ts, level, bins_fm, n_stride);
+    const PartView pv = part_view_of(splits, split_stride, f_eq, level, bins_fm, n_stride);
     const int64_t r0 = (int64_t)blockIdx.x * kRouteTile + (int64_t)threadIdx.x * kRouteRows;
     uint32_t lv[kRouteRows];
     route_rows(level, n, r0, pv, leaf, lv);
@@ -1696,16 +1717,18 @@ __global__ void __launch_bounds__(1024) segments_kernel(int level, int64_t n, co
 }
 
 void launch_partition(int level, int64_t n, const uint8_t* bins_fm, int64_t n_stride, uint16_t* leaf,
-                      const uint8_t* small_side, uint32_t* cursor, uint32_t* list, TreeState* ts, cudaStream_t st) {
+                      const uint8_t* small_side, uint32_t* cursor, uint32_t* list, const int32_t* splits,
+                      int split_stride, int f_eq, cudaStream_t st) {
     const int64_t tiles = (n + kRouteTile - 1) / kRouteTile;
     if (tiles <= 0) return;
     const unsigned g = (unsigned)tiles;
-    if (level == 0)
-        partition_kernel<1><<<g, kRouteThreads, 0, st>>>(level, n, bins_fm, n_stride, ts, leaf, small_side, cursor, list);
-    else if (level == 1)
-        partition_kernel<2><<<g, kRouteThreads, 0, st>>>(level, n, bins_fm, n_stride, ts, leaf, small_side, cursor, list);
-    else
-        partition_kernel<0><<<g, kRouteThreads, 0, st>>>(level, n, bins_fm, n_stride, ts, leaf, small_side, cursor, list);
+#define CBGPU_PART(K)                                                                                        \
+    partition_kernel<K><<<g, kRouteThreads, 0, st>>>(level, n, bins_fm, n_stride, splits, split_stride, f_eq, \
+                                                     leaf, small_side, cursor, list)
+    if (level == 0) CBGPU_PART(1);
+    else if (level == 1) CBGPU_PART(2);
+    else CBGPU_PART(0);
+#undef CBGPU_PART
 }
 
 void launch_segments(int level, int64_t n, const uint32_t* rows_in, const uint32_t* base_in, const uint32_t* cursor,

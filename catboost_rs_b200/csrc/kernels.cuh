@@ -271,9 +271,13 @@ void launch_select_split(int level, int world, int stride, const ull* all_best, 
                          uint8_t* small_side, cudaStream_t st);
 // Routing by split `level` (leaf[] is not read at level 0) and, for each
 // parent q < 2^level, the rows of its built child (new bit == small_side[q])
-// written to list from cursor[q] on (cursor[q] advances past them).
+// written to list from cursor[q] on (cursor[q] advances past them).  The
+// split of level l is (splits[l * split_stride], splits[l * split_stride + 1])
+// = (feature, bin); features >= f_eq are one-hot (bit = bin == value), the
+// others take bit = bin > border.
 void launch_partition(int level, int64_t n, const uint8_t* bins_fm, int64_t n_stride, uint16_t* leaf,
-                      const uint8_t* small_side, uint32_t* cursor, uint32_t* list, TreeState* ts, cudaStream_t st);
+                      const uint8_t* small_side, uint32_t* cursor, uint32_t* list, const int32_t* splits,
+                      int split_stride, int f_eq, cudaStream_t st);
 // After launch_partition(level): the next level's histogram work list from
 // the built segments [base_in[q], cursor[q]) (ts->hist_rows[level + 1]); with
 // rows_out not null, the 2^(level+1) children's row counts and segment starts

@@ -234,6 +234,71 @@ __global__ void mc_pack_kernel(int64_t n, int K, const double* __restrict__ wd1,
             q[(size_t)c * n + i] = llrint(ldexp(mc_channel(c, K, n, i, wd1, weight, s_mode, sw32, sw64), sh));
 }
 
+// ---- histograms over leaf-sorted row lists (every mode but the pairwise
+// scorers): the score channels are packed in pairs at the scalar path's
+// fixed point (max |v| * 2^shift < 2^kPackBits, one shift for all channels),
+// each pair is histogrammed by the scalar path's kernel for the built child
+// of every parent only, the siblings are derived by subtraction, and the
+// level table is laid out as hist[leaf][F][NB][C] for the scorers.
+
+__global__ void mc_shift33_kernel(McState* ms) {
+    ms->hist_shift = fixed_shift(__longlong_as_double((long long)ms->maxbits), kPackBits);
+}
+
+// qp[p][i] = the (lo, hi) parts of channels 2p and 2p + 1 of row i (pack_gh's split).
+__global__ void mc_pack2_kernel(int64_t n, int K, int P, const double* __restrict__ wd1,
+                                const double* __restrict__ weight, int s_mode, const float* __restrict__ sw32,
+                                const double* __restrict__ sw64, const McState* __restrict__ ms,
+                                uint4* __restrict__ qp) {
+    const int sh = ms->hist_shift;
+    const int C = K + 1;
+    const long long mask = (1ll << kPackSplit) - 1;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        for (int p = 0; p < P; ++p) {
+            const long long v0 = llrint(ldexp(mc_channel(2 * p, K, n, i, wd1, weight, s_mode, sw32, sw64), sh));
+            const long long v1 =
+                2 * p + 1 < C ? llrint(ldexp(mc_channel(2 * p + 1, K, n, i, wd1, weight, s_mode, sw32, sw64), sh))
+                              : 0ll;
+            qp[(size_t)p * n + i] = make_uint4((uint32_t)(v0 & mask), (uint32_t)(int32_t)(v0 >> kPackSplit),
+                                               (uint32_t)(v1 & mask), (uint32_t)(int32_t)(v1 >> kPackSplit));
+        }
+}
+
+// hist[q][f][b][c] = cur[c / 2][f][q][b][c % 2] (pair tables `pair_stride` words apart).
+__global__ void mc_gather_kernel(int Q, int F, int NB, int C, const unsigned long long* __restrict__ cur,
+                                 size_t pair_stride, unsigned long long* __restrict__ hist) {
+    const int64_t total = (int64_t)Q * F * NB * C;
+    for (int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < total; k += (int64_t)gridDim.x * blockDim.x) {
+        const int c = (int)(k % C);
+        int64_t t = k / C;
+        const int b = (int)(t % NB);
+        t /= NB;
+        const int f = (int)(t % F);
+        const int q = (int)(t / F);
+        hist[k] = cur[(size_t)(c >> 1) * pair_stride + (((size_t)f * Q + q) * NB + b) * 2 + (c & 1)];
+    }
+}
+
+// The next level's build side of each leaf q: the winner's child with no more
+// weight (channel K).  Float split: TRUE = bins above the border; one-hot:
+// TRUE = the value's own bin, as routing sets the leaf bit.
+__global__ void mc_side_kernel(int level, int F, int NB, int C, int K, int F0,
+                               const unsigned long long* __restrict__ hist, McState* __restrict__ ms,
+                               const TreeState* __restrict__ fts, uint8_t* __restrict__ small_side) {
+    const McSplit sp = ms->split[level];
+    const int Q = 1 << level;
+    for (int q = threadIdx.x; q < Q; q += blockDim.x) {
+        const unsigned long long* row = hist + ((size_t)q * F + sp.feature) * NB * C;
+        const long long wt = (long long)row[(size_t)(NB - 1) * C + K];
+        const long long wp = (long long)row[(size_t)sp.bin * C + K];
+        long long tw;
+        if (sp.feature >= F0) tw = wp - (sp.bin > 0 ? (long long)row[(size_t)(sp.bin - 1) * C + K] : 0ll);
+        else tw = wt - wp;
+        small_side[q] = true_child_built((unsigned long long)(wt - tw), (unsigned long long)tw);
+    }
+    if (threadIdx.x == 0 && fts->err) atomicOr(&ms->err, kMcErrLeafRange);  // a work list outgrew its buffer
+}
+
 // Level histogram: block (feature f, channel c, rows [r0, r0 + kMcChunk)) adds
 // q[c][row] into cell (leaf, f, bin, c) of hist[leaves][F][NB][C].  The
 // leaves x bins table sits in shared memory when it fits (smem > 0), each
@@ -1516,6 +1581,20 @@ struct cbgpu_multi_session {
     double* h_raw = nullptr;
     void* leaf_export = nullptr;
     size_t hist_cells = 0;
+    // histograms over leaf-sorted row lists (all modes but the pairwise scorers)
+    bool fast = false;
+    int fast_pairs = 0, F_pad = 0;
+    uint8_t* bins_rm = nullptr;            // u8 [n][F_pad]
+    uint4* qpairs = nullptr;               // [fast_pairs][n] packed channel pairs
+    unsigned long long* fbuilt = nullptr;  // [fast_pairs][F][slots][NB][2] built children
+    unsigned long long* fcur[2] = {nullptr, nullptr};  // [fast_pairs][F][L/2][NB][2] prefix, two levels
+    size_t fbuilt_cells = 0, fcur_cells = 0;            // per pair
+    uint32_t *flist = nullptr, *fcursor = nullptr, *fseg_rows = nullptr, *fseg_base = nullptr;
+    uint8_t* fside = nullptr;
+    HistChunk *fchunks0 = nullptr, *fchunks = nullptr;
+    uint32_t *fn_chunks0 = nullptr, *fn_chunks = nullptr;
+    size_t fchunk_cap = 0;
+    TreeState* fts = nullptr;  // partition bookkeeping: first cursor, work-list errors
     // ranking mode (grouped losses, K = 1)
     int rank_mode = -1;  // -1: MultiClass; kRankQueryRmse / kRankPairLogit / kRankPairLogitPairwise
     int n_groups = 0;
@@ -1582,6 +1661,21 @@ struct cbgpu_multi_session {
         cudaFree(d_der2);
         cudaFree(d_tgt);
         cudaFree(bins_fm);
+        cudaFree(bins_rm);
+        cudaFree(qpairs);
+        cudaFree(fbuilt);
+        cudaFree(fcur[0]);
+        cudaFree(fcur[1]);
+        cudaFree(flist);
+        cudaFree(fcursor);
+        cudaFree(fseg_rows);
+        cudaFree(fseg_base);
+        cudaFree(fside);
+        cudaFree(fchunks0);
+        cudaFree(fchunks);
+        cudaFree(fn_chunks0);
+        cudaFree(fn_chunks);
+        cudaFree(fts);
         cudaFree(d_bc);
         cudaFree(approx);
         cudaFree(weight);
@@ -1756,6 +1850,44 @@ int begin_impl(const cbgpu_begin_args* a, int32_t K, const float* const* cols, c
     cudaFree(d_err);
     if (rc) return rc;
     MCU(cudaStreamSynchronize(s->st));
+    return CBGPU_OK;
+}
+
+// Buffers of the list-based histograms: row-major bins, packed channel pairs,
+// the built / level tables of every pair, the row list with its per-parent
+// segments, the work lists.  Called once, at the first tree of a mode that
+// uses them.
+int fast_setup(cbgpu_multi_session* s) {
+    const int64_t n = s->n;
+    const int F = s->F, NB = s->NB, C = s->K + 1, L = 1 << s->depth;
+    cudaStream_t st = s->st;
+    s->fast_pairs = (C + 1) / 2;
+    s->F_pad = (F + 31) / 32 * 32;
+    MDA(s->bins_rm, (size_t)std::max<int64_t>(n, 1) * s->F_pad);
+    MDA(s->qpairs, (size_t)s->fast_pairs * std::max<int64_t>(n, 1));
+    s->fbuilt_cells = (size_t)F * std::max(1, L / 4) * NB * 2;
+    s->fcur_cells = (size_t)F * std::max(1, L / 2) * NB * 2;
+    MDA(s->fbuilt, s->fbuilt_cells * s->fast_pairs);
+    MDA(s->fcur[0], s->fcur_cells * s->fast_pairs);
+    MDA(s->fcur[1], s->fcur_cells * s->fast_pairs);
+    MDA(s->flist, std::max<int64_t>(n, 1));
+    MDA(s->fcursor, 2 * kSegMax);
+    MDA(s->fseg_rows, 2 * kSegMax);
+    MDA(s->fseg_base, 2 * kSegMax);
+    MDA(s->fside, kSegMax);
+    s->fchunk_cap = (size_t)(n / kChunkRows) + (L / 2) + 2;
+    MDA(s->fchunks, s->fchunk_cap);
+    MDA(s->fn_chunks, 1);
+    MDA(s->fchunks0, (size_t)(n / kChunkRows) + 2);
+    MDA(s->fn_chunks0, 1);
+    MDA(s->fts, 1);
+    MCU(cudaMemsetAsync(s->fts, 0, sizeof(TreeState), st));
+    if (n > 0) launch_transpose_fm_to_rm(s->bins_fm, n, n, F, s->bins_rm, s->F_pad, st);
+    launch_level0_chunks(n, s->fchunks0, (uint32_t)(n / kChunkRows) + 2, s->fn_chunks0,
+                         (uint32_t*)((char*)s->fts + offsetof(TreeState, err)), st);
+    MCU(cudaGetLastError());
+    MCU(cudaStreamSynchronize(st));
+    s->fast = true;
     return CBGPU_OK;
 }
 
@@ -2305,12 +2437,67 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
     // the histogram weight channel: PairLogit's pairwise weights, else the object weights
     const double* hw = s->rank_mode >= 0 ? s->d_eff : s->weight;
     mc_max_kernel<<<g, kMcThreads, 0, st>>>(n, K, s->wd1, hw, s_mode, s->sw32, s->sw64, s->d_ms);
-    mc_shift_kernel<<<1, 1, 0, st>>>(n, s->d_ms);
-    mc_pack_kernel<<<g, kMcThreads, 0, st>>>(n, K, s->wd1, hw, s_mode, s->sw32, s->sw64, s->d_ms, s->q);
-    MCU(cudaGetLastError());
     const unsigned chunks = (unsigned)((n + kMcChunk - 1) / kMcChunk);
     const bool pairwise = s->rank_mode == kRankPairLogitPairwise || s->rank_mode == kRankYetiRankPairwise;
-    for (int l = 0; l < D; ++l) {
+    if (!pairwise && !s->fast) {
+        int rc = fast_setup(s);
+        if (rc) return rc;
+    }
+    if (!pairwise) {
+        // histograms of the built children over leaf-sorted row lists
+        const int P = s->fast_pairs;
+        mc_shift33_kernel<<<1, 1, 0, st>>>(s->d_ms);
+        mc_pack2_kernel<<<g, kMcThreads, 0, st>>>(n, K, P, s->wd1, hw, s_mode, s->sw32, s->sw64, s->d_ms,
+                                                  s->qpairs);
+        MCU(cudaMemsetAsync(s->fts, 0, sizeof(TreeState), st));
+        MCU(cudaGetLastError());
+        const int32_t* mc_splits = (const int32_t*)((char*)s->d_ms + offsetof(McState, split));
+        int cur = 0;
+        for (int l = 0; l < D; ++l) {
+            const int Q = 1 << l;
+            const size_t slots = l == 0 ? 1 : (size_t)Q / 2;
+            const size_t bcells = (size_t)F * slots * NB * 2;
+            MCU(cudaMemsetAsync(s->fbuilt, 0, sizeof(unsigned long long) * s->fbuilt_cells * P, st));
+            const uint32_t max_chunks = (uint32_t)(n / kChunkRows + slots + 1);
+            for (int p = 0; p < P; ++p)
+                launch_hist(s->bins_rm, s->F_pad, F, NB, s->qpairs + (size_t)p * n, l == 0 ? nullptr : s->flist,
+                            l == 0 ? s->fchunks0 : s->fchunks, l == 0 ? s->fn_chunks0 : s->fn_chunks, max_chunks,
+                            s->fbuilt + (size_t)p * bcells, (int64_t)slots * NB * 2, (int64_t)NB * 2, st);
+            for (int p = 0; p < P; ++p)
+                launch_derive_prefix(l, F, NB, s->fbuilt + (size_t)p * bcells, s->fcur[cur ^ 1] + (size_t)p * s->fcur_cells,
+                                     s->fcur[cur] + (size_t)p * s->fcur_cells, s->fside, st);
+            mc_gather_kernel<<<grid_for((int64_t)Q * F * NB * C), kMcThreads, 0, st>>>(Q, F, NB, C, s->fcur[cur],
+                                                                                     s->fcur_cells, s->hist);
+            mc_score_kernel<<<grid_for((int64_t)F * NB), kMcThreads, 0, st>>>(Q, F, NB, K, s->hist, s->d_bc,
+                                                                              s->d_ms, s->l2, s->score_fn, s->F0,
+                                                                              s->d_present, s->scores);
+            mc_argmax_kernel<<<1, 1024, 0, st>>>((int64_t)F * NB, NB, s->scores, l, s->d_ms);
+            if (l + 1 < D) {
+                mc_side_kernel<<<1, 1024, 0, st>>>(l, F, NB, C, K, s->F0, s->hist, s->d_ms, s->fts, s->fside);
+                const int pp = l & 1, np = pp ^ 1;
+                uint32_t* cur_l = l == 0 ? (uint32_t*)((char*)s->fts + offsetof(TreeState, cursor0))
+                                         : s->fcursor + (size_t)pp * kSegMax;
+                const bool more = l + 2 < D;
+                launch_partition(l, n, s->bins_fm, n, s->leaf, s->fside, cur_l, s->flist, mc_splits, 2, s->F0, st);
+                launch_segments(l, n, l == 0 ? nullptr : s->fseg_rows + (size_t)pp * kSegMax,
+                                l == 0 ? nullptr : s->fseg_base + (size_t)pp * kSegMax, cur_l, s->fside,
+                                more ? s->fseg_rows + (size_t)np * kSegMax : nullptr,
+                                more ? s->fseg_base + (size_t)np * kSegMax : nullptr,
+                                more ? s->fcursor + (size_t)np * kSegMax : nullptr, s->fchunks,
+                                (uint32_t)s->fchunk_cap, s->fn_chunks, s->fts, st);
+            } else {
+                mc_route_kernel<<<g, kMcThreads, 0, st>>>(n, l, s->bins_fm, s->F0, s->d_ms, s->leaf);
+            }
+            MCU(cudaGetLastError());
+            cur ^= 1;
+        }
+    }
+    if (pairwise) {
+        mc_shift_kernel<<<1, 1, 0, st>>>(n, s->d_ms);
+        mc_pack_kernel<<<g, kMcThreads, 0, st>>>(n, K, s->wd1, hw, s_mode, s->sw32, s->sw64, s->d_ms, s->q);
+        MCU(cudaGetLastError());
+    }
+    for (int l = 0; l < D && pairwise; ++l) {
         const int leaves = 1 << l;
         const size_t cells = (size_t)leaves * F * NB * C;
         MCU(cudaMemsetAsync(s->hist, 0, sizeof(unsigned long long) * cells, st));

@@ -640,7 +640,9 @@ int enqueue_tree(cbgpu_session* s, int set, bool prof, int boot_mode, int s_mode
             uint32_t* cur_l = l == 0 ? (uint32_t*)((char*)s->ts + offsetof(TreeState, cursor0))
                                      : s->cursor + (size_t)p * kSegMax;
             const bool more = l + 2 < D;  // another partition follows
-            launch_partition(l, s->n, s->bins_fm, s->n_stride, s->leaf, s->small_side, cur_l, s->list, s->ts, st);
+            launch_partition(l, s->n, s->bins_fm, s->n_stride, s->leaf, s->small_side, cur_l, s->list,
+                             (const int32_t*)((char*)s->ts + offsetof(TreeState, split)),
+                             (int)(sizeof(SplitRec) / sizeof(int32_t)), 0x7fffffff, st);
             launch_segments(l, s->n, l == 0 ? nullptr : s->seg_rows + (size_t)p * kSegMax,
                             l == 0 ? nullptr : s->seg_base + (size_t)p * kSegMax, cur_l, s->small_side,
                             more ? s->seg_rows + (size_t)np * kSegMax : nullptr,

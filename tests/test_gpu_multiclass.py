@@ -101,6 +101,37 @@ def _zipf_cats(rs, n, cards):
     return cols
 
 
+def _leaf_ids(split_feature, split_bin, allbins, F):
+    # routing: floats pass on bin > border, one-hot features on bin == value
+    leaf = np.zeros(allbins.shape[1], dtype=np.int64)
+    for l, (f, b) in enumerate(zip(split_feature, split_bin)):
+        bit = (allbins[f] == b) if f >= F else (allbins[f] > b)
+        leaf |= bit.astype(np.int64) << l
+    return leaf
+
+
+def _assert_same_partitions(m, o, allbins, F, tol):
+    """Trees equal to the oracle's up to exactly tied equivalent one-hot tests:
+    once a parent leaf holds only two categories of a feature, the tests
+    "== a" and "== b" partition it identically with the children swapped,
+    and their scores are equal in exact arithmetic, so the last bit of the
+    rounding picks between them.  Every other split must be identical; the
+    rows must fall into the same parts (a one-to-one relabeling of the
+    leaves) with the same leaf values, and the approximants must agree."""
+    T = o.split_feature.shape[0]
+    np.testing.assert_array_equal(m.split_feature, o.split_feature)
+    for t in range(T):
+        diff = m.split_bin[t] != o.split_bin[t]
+        assert (o.split_feature[t][diff] >= F).all(), (t, m.split_bin[t], o.split_bin[t])
+        lm = _leaf_ids(m.split_feature[t], m.split_bin[t], allbins, F)
+        lo = _leaf_ids(o.split_feature[t], o.split_bin[t], allbins, F)
+        pairs = set(zip(lm.tolist(), lo.tolist()))
+        assert len({a for a, _ in pairs}) == len(pairs) == len({b for _, b in pairs}), t
+        for a, b in pairs:
+            assert np.max(np.abs(m.leaf_values[t, a] - o.leaf_values[t, b])) <= tol, (t, a, b)
+    assert np.max(np.abs(m.staged - o.staged)) <= tol
+
+
 @pytest.mark.parametrize("score,depth", [("Cosine", 5), ("L2", 4)])
 def test_multiclass_one_hot_matches_oracle(cb, score, depth):
     # one-hot categorical features: equality candidates after the floats,
@@ -120,12 +151,9 @@ def test_multiclass_one_hot_matches_oracle(cb, score, depth):
     o = oracle.train_multiclass(bins, [len(b) for b in borders], cls, K, depth=depth, iterations=4,
                                 learning_rate=fp.learning_rate, l2_leaf_reg=fp.l2_leaf_reg, score_function=score,
                                 cat_bins_fm=cat_bins)
-    np.testing.assert_array_equal(m.split_feature, o.split_feature)
-    np.testing.assert_array_equal(m.split_bin, o.split_bin)
+    _assert_same_partitions(m, o, np.concatenate([bins, cat_bins.astype(bins.dtype)]), F, TOL)
     assert (m.split_feature >= F).any()  # one-hot splits were taken
     assert np.isnan(m.split_borders()[m.split_feature >= F]).all()
-    assert np.max(np.abs(m.leaf_values - o.leaf_values)) <= TOL
-    assert np.max(np.abs(m.staged - o.staged)) <= TOL
 
 
 def test_multiclass_one_hot_declines_bootstrap(cb):
