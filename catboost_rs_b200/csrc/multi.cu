@@ -1095,98 +1095,127 @@ __global__ void rk_srank_kernel(int n_groups, const int64_t* __restrict__ goff, 
 
 // ---- YetiRank: per-tree pair sampling on the device --------------------------
 
-// sample_pairs (crates/cb-train/src/yetirank.rs:75-171), one thread per group:
+// sample_pairs (crates/cb-train/src/yetirank.rs:75-171), one warp per group:
 // per permutation one TFastRng64 draw per document (cast to f32, ratio
 // u / (1.000001 - u) in f32) multiplies exp(approx), a stable descending sort,
 // and the Classic decayed weights 0.15 * decay^k * |rel_a - rel_b| (f32) go to
 // the higher-relevance document's row of the group's dense f32 matrix
-// cw[winner][loser].  idx / boot are n-sized scratch indexed by object.
-__global__ void rk_yeti_sample_kernel(int n_groups, const int64_t* __restrict__ goff, const double* __restrict__ ap,
-                                      const double* __restrict__ target, int perms, double decay,
-                                      const uint64_t* __restrict__ seeds, const int64_t* __restrict__ cwoff,
-                                      float* __restrict__ cw, int32_t* __restrict__ idx, double* __restrict__ boot) {
-    const int gi = blockIdx.x * blockDim.x + threadIdx.x;
-    if (gi >= n_groups) return;
+// cw[winner][loser].  Each lane jumps its own copy of the group's stream to
+// its documents' draws (draw p * g + i); the sort is a rank count (position of
+// i = documents with a larger key, or an equal key and a smaller index: the
+// stable descending order); within one permutation the adjacent pairs touch
+// distinct cells, so lanes add them at once, and permutations follow each
+// other in order -- every rounding is the sequential loop's.  decay_pow[k] =
+// decay^k formed by k successive multiplications.  idx / boot are n-sized
+// scratch indexed by object.
+constexpr int kYetiWarps = 4;  // groups per 128-thread block
+
+__global__ void __launch_bounds__(kYetiWarps * 32) rk_yeti_sample_kernel(
+    int n_groups, const int64_t* __restrict__ goff, const double* __restrict__ ap, const double* __restrict__ target,
+    int perms, const double* __restrict__ decay_pow, const uint64_t* __restrict__ seeds,
+    const int64_t* __restrict__ cwoff, float* __restrict__ cw, int32_t* __restrict__ idx,
+    double* __restrict__ boot) {
+    const int lane = threadIdx.x & 31;
+    const int gi = blockIdx.x * kYetiWarps + (threadIdx.x >> 5);
+    if (gi >= n_groups) return;  // warp-uniform
     const int64_t b = goff[gi], g = goff[gi + 1] - b;
     float* cwg = cw + cwoff[gi];
-    for (int64_t k = 0; k < g * g; ++k) cwg[k] = 0.0f;
+    for (int64_t k = lane; k < g * g; k += 32) cwg[k] = 0.0f;
     if (g == 0) return;
-    Rng64 r = Rng64::from_seed(seeds[gi]);
+    const Rng64 base = Rng64::from_seed(seeds[gi]);
     int32_t* ix = idx + b;
     double* bt = boot + b;
+    __syncwarp();
     for (int p = 0; p < perms; ++p) {
-        for (int64_t i = 0; i < g; ++i) {
-            ix[i] = (int32_t)i;
+        for (int64_t i = lane; i < g; i += 32) {
+            Rng64 r = base;
+            r.advance((uint64_t)p * (uint64_t)g + (uint64_t)i);
             const float u = __double2float_rn(real1(r));
             const float ratio = __fdiv_rn(u, __fsub_rn(1.000001f, u));
             bt[i] = __dmul_rn(exp(ap[b + i]), (double)ratio);
         }
-        for (int64_t i = 1; i < g; ++i) {  // stable insertion sort, descending
-            const int32_t key = ix[i];
-            int64_t j = i - 1;
-            while (j >= 0 && bt[ix[j]] < bt[key]) {
-                ix[j + 1] = ix[j];
-                --j;
+        __syncwarp();
+        for (int64_t i = lane; i < g; i += 32) {
+            const double key = bt[i];
+            int64_t pos = 0;
+            for (int64_t j = 0; j < g; ++j) {
+                const double o = bt[j];
+                pos += (o > key || (o == key && j < i)) ? 1 : 0;
             }
-            ix[j + 1] = key;
+            ix[pos] = (int32_t)i;
         }
-        double dc = 1.0;
-        for (int64_t d = 1; d < g; ++d) {
+        __syncwarp();
+        for (int64_t d = 1 + lane; d < g; d += 32) {
             const int32_t first = ix[d - 1], second = ix[d];
             const float rf = __double2float_rn(target[b + first]), rs = __double2float_rn(target[b + second]);
-            const float pw = __double2float_rn(__dmul_rn(__dmul_rn(0.15, dc), (double)fabsf(__fsub_rn(rf, rs))));
+            const float pw =
+                __double2float_rn(__dmul_rn(__dmul_rn(0.15, decay_pow[d - 1]), (double)fabsf(__fsub_rn(rf, rs))));
             if (rf > rs) cwg[first * g + second] = __fadd_rn(cwg[first * g + second], pw);
             else if (rf < rs) cwg[second * g + first] = __fadd_rn(cwg[second * g + first], pw);
-            dc = __dmul_rn(dc, decay);
         }
+        __syncwarp();
     }
 }
 
 // The PairLogit der over one phase's sampled pairs (pairlogit_group_der,
 // ranking_der.rs:400-440), winner rows ascending, losers ascending, pair
 // weight (qw * cw / perms) in f32; eff (when given) gets the pairwise weights
-// (calc_pairwise_weights, boosting.rs:1761-1780) in the same order.
-__global__ void rk_yeti_der_kernel(int n_groups, const int64_t* __restrict__ goff, const double* __restrict__ ap,
-                                   const double* __restrict__ gw, int perms, const int64_t* __restrict__ cwoff,
-                                   const float* __restrict__ cw, double* __restrict__ d1, double* __restrict__ d2,
-                                   double* __restrict__ eff, McState* __restrict__ ms) {
-    const int gi = blockIdx.x * blockDim.x + threadIdx.x;
-    if (gi >= n_groups) return;
+// (calc_pairwise_weights, boosting.rs:1761-1780) in the same order.  One warp
+// per group, one lane per document: a document's der1 / der2 / eff receive
+// its terms in the sequential loop's order (by winner row; its own winner row
+// adds its loser sum at that point), so every sum rounds as the CPU's.  ex is
+// n-sized scratch for exp(approx).
+__global__ void __launch_bounds__(kYetiWarps * 32) rk_yeti_der_kernel(
+    int n_groups, const int64_t* __restrict__ goff, const double* __restrict__ ap, const double* __restrict__ gw,
+    int perms, const int64_t* __restrict__ cwoff, const float* __restrict__ cw, double* __restrict__ d1,
+    double* __restrict__ d2, double* __restrict__ eff, double* __restrict__ ex, McState* __restrict__ ms) {
+    const int lane = threadIdx.x & 31;
+    const int gi = blockIdx.x * kYetiWarps + (threadIdx.x >> 5);
+    if (gi >= n_groups) return;  // warp-uniform
     const int64_t b = goff[gi], g = goff[gi + 1] - b;
     const float* cwg = cw + cwoff[gi];
     const float qw = __double2float_rn(gw[gi]), den = (float)perms;
-    for (int64_t i = b; i < b + g; ++i) {
-        d1[i] = 0.0;
-        d2[i] = 0.0;
-        if (eff) eff[i] = 0.0;
-    }
+    for (int64_t i = lane; i < g; i += 32) ex[b + i] = exp(ap[b + i]);
+    __syncwarp();
     bool finite = true;
-    for (int64_t wl = 0; wl < g; ++wl) {
-        double wd = 0.0, wd2 = 0.0;
-        const double ew = exp(ap[b + wl]);
-        for (int64_t ll = 0; ll < g; ++ll) {
-            const float wf = __fdiv_rn(__fmul_rn(qw, cwg[wl * g + ll]), den);
+    for (int64_t x = lane; x < g; x += 32) {
+        double a1 = 0.0, a2 = 0.0, ae = 0.0;
+        const double ewx = ex[b + x];
+        for (int64_t wl = 0; wl < g; ++wl) {
+            if (wl == x) {  // x as the winner: its losers in ascending order
+                double wd = 0.0, wd2 = 0.0;
+                for (int64_t ll = 0; ll < g; ++ll) {
+                    const float wf = __fdiv_rn(__fmul_rn(qw, cwg[x * g + ll]), den);
+                    if (wf == 0.0f) continue;
+                    const double c = (double)wf;
+                    const double el = ex[b + ll];
+                    const double dn = __dadd_rn(el, ewx);
+                    const double p = dn > 0.0 ? __ddiv_rn(el, dn) : 0.5;
+                    const double cp = __dmul_rn(c, p);
+                    wd = __dadd_rn(wd, cp);
+                    wd2 = __dadd_rn(wd2, __dmul_rn(cp, __dsub_rn(p, 1.0)));
+                    ae = __dadd_rn(ae, c);
+                }
+                a1 = __dadd_rn(a1, wd);
+                a2 = __dadd_rn(a2, wd2);
+                continue;
+            }
+            const float wf = __fdiv_rn(__fmul_rn(qw, cwg[wl * g + x]), den);  // x as a loser of wl
             if (wf == 0.0f) continue;
             const double c = (double)wf;
-            const double el = exp(ap[b + ll]);
-            const double dn = __dadd_rn(el, ew);
-            const double p = dn > 0.0 ? __ddiv_rn(el, dn) : 0.5;
+            const double dn = __dadd_rn(ewx, ex[b + wl]);
+            const double p = dn > 0.0 ? __ddiv_rn(ewx, dn) : 0.5;
             const double cp = __dmul_rn(c, p);
-            const double t = __dmul_rn(cp, __dsub_rn(p, 1.0));
-            wd = __dadd_rn(wd, cp);
-            wd2 = __dadd_rn(wd2, t);
-            d1[b + ll] = __dsub_rn(d1[b + ll], cp);
-            d2[b + ll] = __dadd_rn(d2[b + ll], t);
-            if (eff) {
-                eff[b + wl] = __dadd_rn(eff[b + wl], c);
-                eff[b + ll] = __dadd_rn(eff[b + ll], c);
-            }
+            a1 = __dsub_rn(a1, cp);
+            a2 = __dadd_rn(a2, __dmul_rn(cp, __dsub_rn(p, 1.0)));
+            ae = __dadd_rn(ae, c);
         }
-        d1[b + wl] = __dadd_rn(d1[b + wl], wd);
-        d2[b + wl] = __dadd_rn(d2[b + wl], wd2);
+        d1[b + x] = a1;
+        d2[b + x] = a2;
+        if (eff) eff[b + x] = ae;
+        finite &= isfinite(a1) && isfinite(a2);
     }
-    for (int64_t i = b; i < b + g; ++i) finite &= isfinite(d1[i]) && isfinite(d2[i]);
-    if (!finite) atomicOr(&ms->err, kMcErrNonFinite);
+    if (__any_sync(0xffffffffu, !finite) && lane == 0) atomicOr(&ms->err, kMcErrNonFinite);
 }
 
 // ---- PairLogitPairwise: pairwise split scoring and Cholesky pairwise leaves
@@ -1628,6 +1657,7 @@ struct cbgpu_multi_session {
     int64_t* d_cwoff = nullptr;
     float* d_cw = nullptr;
     double *d_yboot = nullptr, *d_lapprox = nullptr, *d_ylf_raw = nullptr, *d_ylf_lrv = nullptr;
+    double* d_ydecay = nullptr;  // decay^k by successive multiplications, k < largest group
     // StochasticRank: metric / sigma / mu / samples and per-group scratch
     int srank_ndcg = 1, srank_num_est = 1;
     double srank_sigma = 1.0, srank_mu = 0.0;
@@ -1644,6 +1674,7 @@ struct cbgpu_multi_session {
         cudaFree(d_cwoff);
         cudaFree(d_cw);
         cudaFree(d_yboot);
+        cudaFree(d_ydecay);
         cudaFree(d_lapprox);
         cudaFree(d_ylf_raw);
         cudaFree(d_ylf_lrv);
@@ -2151,6 +2182,20 @@ int cbgpu_rank_begin_raw(const cbgpu_begin_args* a, const int64_t* group_offsets
             if (!rc) rc = mdalloc(&s->d_cw, (size_t)std::max<int64_t>(cells, 1));
             if (!rc) rc = mdalloc(&s->d_lmorder, (size_t)n);
             if (!rc) rc = mdalloc(&s->d_yboot, (size_t)n);
+            if (!rc) {
+                int64_t maxg = 1;
+                for (int g = 0; g < n_groups; ++g) maxg = std::max(maxg, group_offsets[g + 1] - group_offsets[g]);
+                std::vector<double> dp((size_t)maxg);
+                double dc = 1.0;  // the sampler's running product, one multiplication per position
+                for (int64_t k = 0; k < maxg; ++k) {
+                    dp[(size_t)k] = dc;
+                    dc = dc * s->yeti_decay;
+                }
+                rc = mdalloc(&s->d_ydecay, (size_t)maxg);
+                if (!rc && cudaMemcpy(s->d_ydecay, dp.data(), sizeof(double) * dp.size(), cudaMemcpyHostToDevice) !=
+                               cudaSuccess)
+                    rc = mfail(CBGPU_ERR_CUDA, "rank_begin: upload failed");
+            }
             if (!rc) rc = mdalloc(&s->d_lapprox, (size_t)n);
             if (!rc) rc = mdalloc(&s->d_ylf_raw, (size_t)1 << a->depth);
             if (!rc) rc = mdalloc(&s->d_ylf_lrv, (size_t)1 << a->depth);
@@ -2373,6 +2418,7 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
     const bool yeti = s->rank_mode == kRankYetiRank || s->rank_mode == kRankYetiRankPairwise;
     const bool srank = s->rank_mode == kRankStochasticRank;
     const unsigned yg = (unsigned)((s->n_groups + 127) / 128);
+    const unsigned yw = (unsigned)((s->n_groups + kYetiWarps - 1) / kYetiWarps);  // a warp per group
     uint64_t srank_base[2] = {0, 0};
     if (yeti || srank) {
         // YetiRankTreeSeeder::next_tree (yetirank.rs:340-430) on the host: the
@@ -2410,11 +2456,11 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
     if (yeti) {
         // gradient / split ders and the histogram's pairwise weights from pairs
         // sampled off the learning-fold approximant
-        rk_yeti_sample_kernel<<<yg, 128, 0, st>>>(s->n_groups, s->d_goff, s->d_lapprox, s->d_tgt, s->yeti_perms,
-                                                 s->yeti_decay, s->d_yseeds, s->d_cwoff, s->d_cw, s->d_lmorder,
+        rk_yeti_sample_kernel<<<yw, kYetiWarps * 32, 0, st>>>(s->n_groups, s->d_goff, s->d_lapprox, s->d_tgt, s->yeti_perms,
+                                                 s->d_ydecay, s->d_yseeds, s->d_cwoff, s->d_cw, s->d_lmorder,
                                                  s->d_yboot);
-        rk_yeti_der_kernel<<<yg, 128, 0, st>>>(s->n_groups, s->d_goff, s->d_lapprox, s->d_gw, s->yeti_perms,
-                                              s->d_cwoff, s->d_cw, s->wd1, s->d_der2, s->d_eff, s->d_ms);
+        rk_yeti_der_kernel<<<yw, kYetiWarps * 32, 0, st>>>(s->n_groups, s->d_goff, s->d_lapprox, s->d_gw, s->yeti_perms,
+                                              s->d_cwoff, s->d_cw, s->wd1, s->d_der2, s->d_eff, s->d_yboot, s->d_ms);
     } else if (srank) {
         rk_srank_kernel<<<yg, 128, 0, st>>>(s->n_groups, s->d_goff, s->approx, s->d_tgt, s->srank_ndcg, s->srank_sigma,
                                            s->srank_mu, s->srank_num_est, srank_base[0], s->d_lmden, s->d_lmideal,
@@ -2541,11 +2587,11 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
         // Newton leaves over the grouped ders, then normalize_leaf_values; the
         // leaf-value recomputes come first so the leaf fixed point sees their ders
         if (yeti) {  // the stored leaves come from pairs sampled off the model approximant
-            rk_yeti_sample_kernel<<<yg, 128, 0, st>>>(s->n_groups, s->d_goff, s->approx, s->d_tgt, s->yeti_perms,
-                                                     s->yeti_decay, s->d_yseeds + 2 * (size_t)s->n_groups, s->d_cwoff,
+            rk_yeti_sample_kernel<<<yw, kYetiWarps * 32, 0, st>>>(s->n_groups, s->d_goff, s->approx, s->d_tgt, s->yeti_perms,
+                                                     s->d_ydecay, s->d_yseeds + 2 * (size_t)s->n_groups, s->d_cwoff,
                                                      s->d_cw, s->d_lmorder, s->d_yboot);
-            rk_yeti_der_kernel<<<yg, 128, 0, st>>>(s->n_groups, s->d_goff, s->approx, s->d_gw, s->yeti_perms,
-                                                  s->d_cwoff, s->d_cw, s->wd1, s->d_der2, nullptr, s->d_ms);
+            rk_yeti_der_kernel<<<yw, kYetiWarps * 32, 0, st>>>(s->n_groups, s->d_goff, s->approx, s->d_gw, s->yeti_perms,
+                                                  s->d_cwoff, s->d_cw, s->wd1, s->d_der2, nullptr, s->d_yboot, s->d_ms);
         }
         if (srank)  // the leaf-value recompute with the leaf-value base
             rk_srank_kernel<<<yg, 128, 0, st>>>(s->n_groups, s->d_goff, s->approx, s->d_tgt, s->srank_ndcg,
@@ -2572,11 +2618,11 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
         }
         if (yeti) {
             // the learning fold: its own resample, Newton deltas x lr, no centring
-            rk_yeti_sample_kernel<<<yg, 128, 0, st>>>(s->n_groups, s->d_goff, s->d_lapprox, s->d_tgt, s->yeti_perms,
-                                                     s->yeti_decay, s->d_yseeds + (size_t)s->n_groups, s->d_cwoff,
+            rk_yeti_sample_kernel<<<yw, kYetiWarps * 32, 0, st>>>(s->n_groups, s->d_goff, s->d_lapprox, s->d_tgt, s->yeti_perms,
+                                                     s->d_ydecay, s->d_yseeds + (size_t)s->n_groups, s->d_cwoff,
                                                      s->d_cw, s->d_lmorder, s->d_yboot);
-            rk_yeti_der_kernel<<<yg, 128, 0, st>>>(s->n_groups, s->d_goff, s->d_lapprox, s->d_gw, s->yeti_perms,
-                                                  s->d_cwoff, s->d_cw, s->wd1, s->d_der2, nullptr, s->d_ms);
+            rk_yeti_der_kernel<<<yw, kYetiWarps * 32, 0, st>>>(s->n_groups, s->d_goff, s->d_lapprox, s->d_gw, s->yeti_perms,
+                                                  s->d_cwoff, s->d_cw, s->wd1, s->d_der2, nullptr, s->d_yboot, s->d_ms);
             rk_leafsum_seq_kernel<<<L, kSeqThreads, 0, st>>>(n, L, s->wd1, s->d_der2, s->weight, s->leaf, 0, rsum,
                                                              s->d_ms);
             if (pairwise) {  // YetiRankPairwise: Cholesky deltas for the learning fold too
