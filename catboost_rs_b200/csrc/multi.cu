@@ -117,6 +117,30 @@ struct McState {
 
 // ---- kernels ---------------------------------------------------------------
 
+// Exclusive block-wide scan of one u32 per thread (blockDim a multiple of 32).
+__device__ __forceinline__ uint32_t block_excl_scan_u32(uint32_t v, uint32_t* sm) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    uint32_t inc = v;
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t t = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += t;
+    }
+    if (lane == 31) sm[w] = inc;
+    __syncthreads();
+    if (w == 0) {
+        uint32_t x = lane < nw ? sm[lane] : 0u;
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t t = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x += t;
+        }
+        sm[lane] = x;
+    }
+    __syncthreads();
+    const uint32_t off = w ? sm[w - 1] : 0u;
+    __syncthreads();
+    return off + inc - v;
+}
+
 // Softmax probabilities of one object (loss.rs:424-455): max-subtracted exp,
 // sequential sum, division.
 __device__ __forceinline__ void mc_softmax(const double* __restrict__ approx, int64_t n, int64_t i, int K,
@@ -819,81 +843,150 @@ __global__ void rk_der_kernel(int n_groups, int mode, const int64_t* __restrict_
     if (!finite) atomicOr(&ms->err, kMcErrNonFinite);
 }
 
-// Per-leaf sums of der1, der2 (unit leaf weights for Newton, boosting.rs:
-// 8345-8380) -- or, for Gradient leaves (count = 1), the row count -- and of
-// the object weight (normalize_leaf_values' leaf weights, boosting.rs:
-// 8525-8540): sums[leaf][3], each accumulated in f64 in object order exactly
-// as the CPU's `sum[leaf[i]] += v[i]` loop does, so the leaf values round as
-// the CPU's.  Grouped ders are discontinuous where two approximants tie
-// (LambdaMart's stable sort and its `same` rule), and the CPU keeps exact
-// cross-leaf ties (a leaf of only winners gets exactly -2 x the Hessian sum
-// as its der1 sum); a sum rounded any other way can split such a tie.
-// One block per leaf: each step compacts the leaf's members of 1024
-// consecutive rows into shared memory in row order (block scan of the
-// per-thread counts); thread 0 then runs the three sequential chains.
-constexpr int kSeqThreads = 256, kSeqRows = 4;
-__global__ void __launch_bounds__(kSeqThreads)
-rk_leafsum_seq_kernel(int64_t n, int L, const double* __restrict__ d1, const double* __restrict__ d2,
-                      const double* __restrict__ weight, const uint16_t* __restrict__ leaf, int count,
-                      double* __restrict__ sums, McState* __restrict__ ms) {
-    constexpr int kStep = kSeqThreads * kSeqRows;
-    __shared__ double v1[kStep], v2[kStep], v3[kStep];
-    __shared__ int wsum[kSeqThreads / 32 + 1];
-    const int q = blockIdx.x, tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-    double s1 = 0.0, s2 = 0.0, s3 = 0.0;
+// Ranking-mode leaf sums: per leaf the sums of der1, der2 (unit leaf weights
+// for Newton, boosting.rs:8345-8380) -- or, for Gradient leaves (count = 1),
+// the row count -- and of the object weight (normalize_leaf_values' leaf
+// weights, boosting.rs:8525-8540), sums[leaf][3], each accumulated in f64 in
+// object order exactly as the CPU's `sum[leaf[i]] += v[i]` loop does, so the
+// leaf values round as the CPU's (exact ties in the approximants survive,
+// which LambdaMart's pair order depends on).  Through a stable counting sort
+// by leaf: rows are counted per
+// (tile, leaf), the counts scanned (leaf-major, then by tile), each tile
+// writes its rows' three values to its leaves' runs in object order (warps in
+// order, lanes in order within a warp), and one thread per leaf adds its run
+// front to back -- the CPU's additions in the CPU's order, with each row
+// read a bounded number of times.
+constexpr int kLsTile = 4096;      // rows per tile (256 threads x 16)
+constexpr int kLsThreads = 256;
+constexpr int kLsMaxLeaves = 1024;
+
+__global__ void __launch_bounds__(kLsThreads) rk_leafcount_kernel(int64_t n, int L, const uint16_t* __restrict__ leaf,
+                                                                  uint32_t* __restrict__ counts,
+                                                                  McState* __restrict__ ms) {
+    __shared__ uint32_t c[kLsMaxLeaves];
+    for (int q = threadIdx.x; q < L; q += blockDim.x) c[q] = 0u;
+    __syncthreads();
+    const int64_t r0 = (int64_t)blockIdx.x * kLsTile;
     bool bad = false;
-    for (int64_t base = 0; base < n; base += kStep) {
-        const int64_t r0 = base + (int64_t)tid * kSeqRows;
-        uint32_t lq[kSeqRows];
-#pragma unroll
-        for (int j = 0; j < kSeqRows; ++j) lq[j] = r0 + j < n ? leaf[r0 + j] : 0xffffu;
-        int m = 0;
-#pragma unroll
-        for (int j = 0; j < kSeqRows; ++j) {
-            m += lq[j] == (uint32_t)q ? 1 : 0;
-            bad |= lq[j] != 0xffffu && lq[j] >= (uint32_t)L;
-        }
-        int inc = m;  // inclusive warp scan, then the warp offsets
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int t = __shfl_up_sync(0xffffffffu, inc, o);
-            if (lane >= o) inc += t;
-        }
-        if (lane == 31) wsum[wid] = inc;
-        __syncthreads();
-        if (tid == 0) {
-            int acc = 0;
-            for (int w = 0; w < kSeqThreads / 32; ++w) {
-                const int t = wsum[w];
-                wsum[w] = acc;
-                acc += t;
-            }
-            wsum[kSeqThreads / 32] = acc;
-        }
-        __syncthreads();
-        int pos = wsum[wid] + inc - m;
-#pragma unroll
-        for (int j = 0; j < kSeqRows; ++j)
-            if (lq[j] == (uint32_t)q) {
-                const int64_t i = r0 + j;
-                v1[pos] = d1[i];
-                v2[pos] = count ? 1.0 : __dmul_rn(d2[i], 1.0);
-                v3[pos] = weight ? weight[i] : 1.0;
-                ++pos;
-            }
-        __syncthreads();
-        if (tid == 0) {
-            const int tot = wsum[kSeqThreads / 32];
-            for (int k = 0; k < tot; ++k) {
-                s1 = __dadd_rn(s1, v1[k]);
-                s2 = __dadd_rn(s2, v2[k]);
-                s3 = __dadd_rn(s3, v3[k]);
-            }
-        }
-        __syncthreads();
+    for (int64_t i = r0 + threadIdx.x; i < r0 + kLsTile && i < n; i += blockDim.x) {
+        const uint32_t q = leaf[i];
+        if (q < (uint32_t)L) atomicAdd(&c[q], 1u);
+        else bad = true;
     }
     if (bad) atomicOr(&ms->err, kMcErrLeafRange);
-    if (tid == 0) {
+    __syncthreads();
+    for (int q = threadIdx.x; q < L; q += blockDim.x) counts[(size_t)blockIdx.x * L + q] = c[q];
+}
+
+// offs[tile][q] = start of tile's rows of leaf q in the leaf-major order;
+// begin[q] / len[q] = leaf q's run.  One block; a thread per leaf walks the tiles.
+__global__ void __launch_bounds__(kLsMaxLeaves) rk_leafscan_kernel(int tiles, int L, const uint32_t* __restrict__ counts,
+                                                                   uint32_t* __restrict__ offs,
+                                                                   uint32_t* __restrict__ begin,
+                                                                   uint32_t* __restrict__ len) {
+    __shared__ uint32_t s_scan[40];
+    const int q = threadIdx.x;
+    uint32_t tot = 0;
+    if (q < L)
+        for (int t = 0; t < tiles; ++t) tot += counts[(size_t)t * L + q];
+    const uint32_t base = block_excl_scan_u32(q < L ? tot : 0u, s_scan);
+    if (q < L) {
+        begin[q] = base;
+        len[q] = tot;
+        uint32_t at = base;
+        for (int t = 0; t < tiles; ++t) {
+            offs[(size_t)t * L + q] = at;
+            at += counts[(size_t)t * L + q];
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kLsThreads) rk_leafscatter_kernel(int64_t n, int L, const uint16_t* __restrict__ leaf,
+                                                                    const uint32_t* __restrict__ offs,
+                                                                    const double* __restrict__ d1,
+                                                                    const double* __restrict__ d2,
+                                                                    const double* __restrict__ weight, int count,
+                                                                    double* __restrict__ v1, double* __restrict__ v2,
+                                                                    double* __restrict__ v3) {
+    constexpr int kW = kLsThreads / 32, kRows = kLsTile / kW;  // each warp: kRows consecutive rows
+    __shared__ uint32_t wc[kW][kLsMaxLeaves];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    for (int k = threadIdx.x; k < kW * L; k += blockDim.x) wc[k / L][k % L] = 0u;
+    __syncthreads();
+    const int64_t r0 = (int64_t)blockIdx.x * kLsTile + (int64_t)w * kRows;
+    for (int j = 0; j < kRows; j += 32) {  // this warp's counts per leaf
+        const int64_t i = r0 + j + lane;
+        const uint32_t q = i < n ? leaf[i] : 0xffffu;
+        const unsigned m = __match_any_sync(0xffffffffu, q);
+        if (q < (uint32_t)L && (m & ((1u << lane) - 1u)) == 0u) wc[w][q] += (uint32_t)__popc(m);
+        __syncwarp();
+    }
+    __syncthreads();
+    for (int q = threadIdx.x; q < L; q += blockDim.x) {  // warp starts in row order
+        uint32_t at = offs[(size_t)blockIdx.x * L + q];
+        for (int k = 0; k < kW; ++k) {
+            const uint32_t c = wc[k][q];
+            wc[k][q] = at;
+            at += c;
+        }
+    }
+    __syncthreads();
+    for (int j = 0; j < kRows; j += 32) {
+        const int64_t i = r0 + j + lane;
+        const uint32_t q = i < n ? leaf[i] : 0xffffu;
+        const unsigned m = __match_any_sync(0xffffffffu, q);
+        if (q < (uint32_t)L) {
+            const uint32_t pos = wc[w][q] + (uint32_t)__popc(m & ((1u << lane) - 1u));
+            v1[pos] = d1[i];
+            v2[pos] = count ? 1.0 : __dmul_rn(d2[i], 1.0);
+            v3[pos] = weight ? weight[i] : 1.0;
+        }
+        __syncwarp();
+        if (q < (uint32_t)L && (m & ((1u << lane) - 1u)) == 0u) wc[w][q] += (uint32_t)__popc(m);
+        __syncwarp();
+    }
+}
+
+// One block per leaf: the run is staged into shared memory a chunk at a time
+// (coalesced loads by every thread, the next chunk's loads in flight while
+// thread 0 adds the current one in order).
+constexpr int kLsRunChunk = 2048;
+
+__global__ void __launch_bounds__(kLsThreads) rk_leafsum_runs_kernel(int L, const uint32_t* __restrict__ begin,
+                                                                     const uint32_t* __restrict__ len,
+                                                                     const double* __restrict__ v1,
+                                                                     const double* __restrict__ v2,
+                                                                     const double* __restrict__ v3,
+                                                                     double* __restrict__ sums) {
+    __shared__ double c1[2][kLsRunChunk / 2], c2[2][kLsRunChunk / 2], c3[2][kLsRunChunk / 2];
+    constexpr int kC = kLsRunChunk / 2;  // values per stage
+    const int q = blockIdx.x;
+    const uint32_t b = begin[q], m = len[q];
+    double s1 = 0.0, s2 = 0.0, s3 = 0.0;
+    auto stage = [&](uint32_t at, int buf) {
+        for (uint32_t k = threadIdx.x; k < kC && at + k < m; k += blockDim.x) {
+            c1[buf][k] = v1[b + at + k];
+            c2[buf][k] = v2[b + at + k];
+            c3[buf][k] = v3[b + at + k];
+        }
+    };
+    if (m > 0) stage(0, 0);
+    __syncthreads();
+    int buf = 0;
+    for (uint32_t at = 0; at < m; at += kC) {
+        if (at + kC < m) stage(at + kC, buf ^ 1);  // the next chunk, while thread 0 adds this one
+        if (threadIdx.x == 0) {
+            const uint32_t cnt = m - at < (uint32_t)kC ? m - at : (uint32_t)kC;
+            for (uint32_t k = 0; k < cnt; ++k) {
+                s1 = __dadd_rn(s1, c1[buf][k]);
+                s2 = __dadd_rn(s2, c2[buf][k]);
+                s3 = __dadd_rn(s3, c3[buf][k]);
+            }
+        }
+        __syncthreads();
+        buf ^= 1;
+    }
+    if (threadIdx.x == 0) {
         sums[3 * q] = s1;
         sums[3 * q + 1] = s2;
         sums[3 * q + 2] = s3;
@@ -1175,6 +1268,8 @@ __global__ void __launch_bounds__(kYetiWarps * 32) rk_yeti_der_kernel(
     const int64_t b = goff[gi], g = goff[gi + 1] - b;
     const float* cwg = cw + cwoff[gi];
     const float qw = __double2float_rn(gw[gi]), den = (float)perms;
+    // a zero cell gives wf == 0 (skipped) whenever qw is finite: skip it before dividing
+    const bool qw_finite = isfinite(qw);
     for (int64_t i = lane; i < g; i += 32) ex[b + i] = exp(ap[b + i]);
     __syncwarp();
     bool finite = true;
@@ -1185,7 +1280,9 @@ __global__ void __launch_bounds__(kYetiWarps * 32) rk_yeti_der_kernel(
             if (wl == x) {  // x as the winner: its losers in ascending order
                 double wd = 0.0, wd2 = 0.0;
                 for (int64_t ll = 0; ll < g; ++ll) {
-                    const float wf = __fdiv_rn(__fmul_rn(qw, cwg[x * g + ll]), den);
+                    const float cv = cwg[x * g + ll];
+                    if (cv == 0.0f && qw_finite) continue;
+                    const float wf = __fdiv_rn(__fmul_rn(qw, cv), den);
                     if (wf == 0.0f) continue;
                     const double c = (double)wf;
                     const double el = ex[b + ll];
@@ -1200,7 +1297,9 @@ __global__ void __launch_bounds__(kYetiWarps * 32) rk_yeti_der_kernel(
                 a2 = __dadd_rn(a2, wd2);
                 continue;
             }
-            const float wf = __fdiv_rn(__fmul_rn(qw, cwg[wl * g + x]), den);  // x as a loser of wl
+            const float cv = cwg[wl * g + x];  // x as a loser of wl
+            if (cv == 0.0f && qw_finite) continue;
+            const float wf = __fdiv_rn(__fmul_rn(qw, cv), den);
             if (wf == 0.0f) continue;
             const double c = (double)wf;
             const double dn = __dadd_rn(ewx, ex[b + wl]);
@@ -1533,7 +1632,7 @@ __global__ void rk_yeti_pairleafw_kernel(int n_groups, const int64_t* __restrict
 }
 
 // Cholesky pairwise leaves (compute_pairwise_leaf_deltas, pairwise_leaves.rs:
-// 219-242) from the leaf der sums (rk_leafsum_seq_kernel's channel 0) with the raw
+// 219-242) from the leaf der sums (rk_leafsums' channel 0) with the raw
 // l2, one block; the seam gets these deltas, the approximant
 // normalize_leaf_values' document-weighted centring x lr (boosting.rs:
 // 2844-2880).  scratch: pw_scratch_doubles(L).
@@ -1658,6 +1757,10 @@ struct cbgpu_multi_session {
     float* d_cw = nullptr;
     double *d_yboot = nullptr, *d_lapprox = nullptr, *d_ylf_raw = nullptr, *d_ylf_lrv = nullptr;
     double* d_ydecay = nullptr;  // decay^k by successive multiplications, k < largest group
+    // ranking leaf sums through a stable sort by leaf: per-(tile, leaf) counts
+    // and offsets, leaf runs, the three value arrays
+    uint32_t *d_lscnt = nullptr, *d_lsoff = nullptr, *d_lsrun = nullptr;
+    double* d_lsval = nullptr;
     // StochasticRank: metric / sigma / mu / samples and per-group scratch
     int srank_ndcg = 1, srank_num_est = 1;
     double srank_sigma = 1.0, srank_mu = 0.0;
@@ -1675,6 +1778,10 @@ struct cbgpu_multi_session {
         cudaFree(d_cw);
         cudaFree(d_yboot);
         cudaFree(d_ydecay);
+        cudaFree(d_lscnt);
+        cudaFree(d_lsoff);
+        cudaFree(d_lsrun);
+        cudaFree(d_lsval);
         cudaFree(d_lapprox);
         cudaFree(d_ylf_raw);
         cudaFree(d_ylf_lrv);
@@ -1881,6 +1988,32 @@ int begin_impl(const cbgpu_begin_args* a, int32_t K, const float* const* cols, c
     cudaFree(d_err);
     if (rc) return rc;
     MCU(cudaStreamSynchronize(s->st));
+    return CBGPU_OK;
+}
+
+// Per-leaf sequential f64 sums (der1, der2 or the row count, weight) of the
+// ranking arm in object order, through the stable sort by leaf.
+int rk_leafsums(cbgpu_multi_session* s, int count, double* sums, cudaStream_t st) {
+    const int64_t n = s->n;
+    const int L = 1 << s->depth;
+    const int tiles = (int)((n + kLsTile - 1) / kLsTile);
+    if (tiles == 0) {
+        MCU(cudaMemsetAsync(sums, 0, sizeof(double) * 3 * (size_t)L, st));
+        return CBGPU_OK;
+    }
+    if (!s->d_lscnt) {
+        MDA(s->d_lscnt, (size_t)tiles * L);
+        MDA(s->d_lsoff, (size_t)tiles * L);
+        MDA(s->d_lsrun, 2 * (size_t)L);
+        MDA(s->d_lsval, 3 * (size_t)n);
+    }
+    double* v = s->d_lsval;
+    rk_leafcount_kernel<<<tiles, kLsThreads, 0, st>>>(n, L, s->leaf, s->d_lscnt, s->d_ms);
+    rk_leafscan_kernel<<<1, kLsMaxLeaves, 0, st>>>(tiles, L, s->d_lscnt, s->d_lsoff, s->d_lsrun, s->d_lsrun + L);
+    rk_leafscatter_kernel<<<tiles, kLsThreads, 0, st>>>(n, L, s->leaf, s->d_lsoff, s->wd1, s->d_der2, s->weight, count,
+                                                        v, v + n, v + 2 * n);
+    rk_leafsum_runs_kernel<<<L, kLsThreads, 0, st>>>(L, s->d_lsrun, s->d_lsrun + L, v, v + n, v + 2 * n, sums);
+    MCU(cudaGetLastError());
     return CBGPU_OK;
 }
 
@@ -2600,8 +2733,10 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
                                                s->d_der2, s->d_ms);
         const int gradient = (s->rank_mode == kRankQuerySoftMax || srank) ? 1 : 0;
         double* rsum = reinterpret_cast<double*>(s->sums);  // 3 f64 per leaf in the ranking mode
-        rk_leafsum_seq_kernel<<<L, kSeqThreads, 0, st>>>(n, L, s->wd1, s->d_der2, s->weight, s->leaf, gradient, rsum,
-                                                         s->d_ms);
+        {
+            int rc = rk_leafsums(s, gradient, rsum, st);
+            if (rc) return rc;
+        }
         if (pairwise) {
             MCU(cudaMemsetAsync(s->d_pwsum, 0, sizeof(long long) * (size_t)L * L, st));
             if (yeti)
@@ -2623,8 +2758,10 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
                                                      s->d_cw, s->d_lmorder, s->d_yboot);
             rk_yeti_der_kernel<<<yw, kYetiWarps * 32, 0, st>>>(s->n_groups, s->d_goff, s->d_lapprox, s->d_gw, s->yeti_perms,
                                                   s->d_cwoff, s->d_cw, s->wd1, s->d_der2, nullptr, s->d_yboot, s->d_ms);
-            rk_leafsum_seq_kernel<<<L, kSeqThreads, 0, st>>>(n, L, s->wd1, s->d_der2, s->weight, s->leaf, 0, rsum,
-                                                             s->d_ms);
+            {
+                int rc = rk_leafsums(s, 0, rsum, st);
+                if (rc) return rc;
+            }
             if (pairwise) {  // YetiRankPairwise: Cholesky deltas for the learning fold too
                 MCU(cudaMemsetAsync(s->d_pwsum, 0, sizeof(long long) * (size_t)L * L, st));
                 rk_yeti_pairleafw_kernel<<<yg, 128, 0, st>>>(s->n_groups, s->d_goff, s->d_cwoff, s->d_cw, s->d_gw,
