@@ -407,39 +407,40 @@ __global__ void mc_score_kernel(int parents, int F, int NB, int K, const unsigne
             scores[k] = -INFINITY;
             continue;
         }
+        // one walk over the (dimension, side, leaf) terms feeds both sums, each
+        // in the CPU's order (the numerator's and the denominator's passes see
+        // the same terms in the same sequence)
         double num = 0.0, den = 1e-100;
-        for (int pass = 0; pass < 2; ++pass) {
-            for (int d = 0; d < K; ++d) {
-                for (int side = 0; side < 2; ++side) {  // false children, then true children
-                    for (int q = 0; q < parents; ++q) {
-                        const unsigned long long* row = pre + ((size_t)q * F + f) * NB * C;
-                        long long wp = (long long)row[(size_t)b * C + K];
-                        const long long wt = (long long)row[(size_t)(NB - 1) * C + K];
-                        long long sp = (long long)row[(size_t)b * C + d];
-                        const long long st = (long long)row[(size_t)(NB - 1) * C + d];
-                        double w, s;
-                        if (cat) {  // the bin's own cell: TRUE = cell, FALSE = total - cell
-                            if (b > 0) {
-                                wp -= (long long)row[(size_t)(b - 1) * C + K];
-                                sp -= (long long)row[(size_t)(b - 1) * C + d];
-                            }
-                            w = __dmul_rn((double)(side ? wp : wt - wp), inv);
-                            s = __dmul_rn((double)(side ? sp : st - sp), inv);
-                        } else {
-                            w = __dmul_rn((double)(side ? wt - wp : wp), inv);
-                            s = __dmul_rn((double)(side ? st - sp : sp), inv);
+        const bool cosine = score_fn == CBGPU_SCORE_COSINE;
+        for (int d = 0; d < K; ++d) {
+            for (int side = 0; side < 2; ++side) {  // false children, then true children
+                for (int q = 0; q < parents; ++q) {
+                    const unsigned long long* row = pre + ((size_t)q * F + f) * NB * C;
+                    long long wp = (long long)row[(size_t)b * C + K];
+                    const long long wt = (long long)row[(size_t)(NB - 1) * C + K];
+                    long long sp = (long long)row[(size_t)b * C + d];
+                    const long long st = (long long)row[(size_t)(NB - 1) * C + d];
+                    double w, s;
+                    if (cat) {  // the bin's own cell: TRUE = cell, FALSE = total - cell
+                        if (b > 0) {
+                            wp -= (long long)row[(size_t)(b - 1) * C + K];
+                            sp -= (long long)row[(size_t)(b - 1) * C + d];
                         }
-                        if (score_fn > 1) {  // SolarL2 / LOOL2 / SatL2: per-leaf terms, no l2
-                            num = __dadd_rn(num, gpu_score_term(score_fn, s, w));
-                            continue;
-                        }
-                        const double avg = mc_avg(s, w, l2);
-                        if (pass == 0) num = __dadd_rn(num, __dmul_rn(avg, s));
-                        else den = __dadd_rn(den, __dmul_rn(__dmul_rn(avg, avg), w));
+                        w = __dmul_rn((double)(side ? wp : wt - wp), inv);
+                        s = __dmul_rn((double)(side ? sp : st - sp), inv);
+                    } else {
+                        w = __dmul_rn((double)(side ? wt - wp : wp), inv);
+                        s = __dmul_rn((double)(side ? st - sp : sp), inv);
                     }
+                    if (score_fn > 1) {  // SolarL2 / LOOL2 / SatL2: per-leaf terms, no l2
+                        num = __dadd_rn(num, gpu_score_term(score_fn, s, w));
+                        continue;
+                    }
+                    const double avg = mc_avg(s, w, l2);
+                    num = __dadd_rn(num, __dmul_rn(avg, s));
+                    if (cosine) den = __dadd_rn(den, __dmul_rn(__dmul_rn(avg, avg), w));
                 }
             }
-            if (score_fn != CBGPU_SCORE_COSINE) break;
         }
         scores[k] = score_fn != CBGPU_SCORE_COSINE ? num : __ddiv_rn(num, sqrt(den));
     }

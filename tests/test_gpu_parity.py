@@ -175,6 +175,9 @@ CASES = [
     dict(n=40000, F=20, loss="RMSE", depth=6, boot="MVS", score="L2", nan=0.02, it=6),
     dict(n=9000, F=50, loss="Logloss", depth=8, boot="Bayesian", score="Cosine", nan=0.05, it=4),
     dict(n=2048, F=5, loss="CrossEntropy", depth=10, boot="No", score="Cosine", nan=0.0, it=3),
+    # past 256 parents the partition reserves one slot per row, past 1024
+    # leaves the final route adds leaf sums with global atomics
+    dict(n=30000, F=8, loss="RMSE", depth=12, boot="Bayesian", score="Cosine", nan=0.02, it=2),
     # few rows per (chunk, tile) item at every level (as on one shard of a
     # multi-GPU fit): 4096-row chunks, and 64- + 32- + 4-feature tiles
     dict(n=200000, F=100, loss="Logloss", depth=8, boot="Bayesian", score="Cosine", nan=0.05, it=2),
