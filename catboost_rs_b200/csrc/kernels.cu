@@ -168,7 +168,8 @@ __global__ void transpose_fm_rm_kernel(const uint8_t* __restrict__ fm, int64_t n
 
 void launch_transpose_fm_to_rm(const uint8_t* fm, int64_t n, int64_t n_stride, int32_t F,
                                uint8_t* rm, int32_t F_pad, cudaStream_t st) {
-    dim3 grid((unsigned)((n + 127) / 128), (unsigned)(F_pad / 32));
+    // columns [0, round_up(F, 32)) of each F_pad-byte row: the F features, zeros after
+    dim3 grid((unsigned)((n + 127) / 128), (unsigned)((F + 31) / 32));
     if (grid.x == 0) return;
     transpose_fm_rm_kernel<<<grid, 256, 0, st>>>(fm, n, n_stride, F, rm, F_pad);
 }
@@ -876,8 +877,13 @@ __global__ void __launch_bounds__(kWarps * 32, 1) hist_kernel(
     const uint8_t* __restrict__ bins_rm, int32_t F_pad, int32_t F, int32_t B,
     const uint4* __restrict__ qstats, const uint32_t* __restrict__ perm,
     const HistChunk* __restrict__ chunks, const uint32_t* __restrict__ n_chunks,
-    ull* __restrict__ built, int64_t feat_stride, int64_t slot_stride) {
+    ull* __restrict__ built, int64_t feat_stride, int64_t slot_stride, int64_t set_qstride,
+    int64_t set_built_stride) {
     extern __shared__ __align__(16) uint32_t hs[];  // table [B][4][32*fpl] then the staging ring
+    // blockIdx.z = stat set: sets share the rows and their bins, each has its
+    // own packed stats and output table
+    qstats += (int64_t)blockIdx.z * set_qstride;
+    built += (int64_t)blockIdx.z * set_built_stride;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     constexpr int kSlice = 32 * kFplFull;  // staged bytes per row
     const size_t table_words = (size_t)B * 128 * kFplFull;
@@ -995,30 +1001,45 @@ static HistShape hist_shape(int32_t B) {
 size_t hist_smem_bytes(int32_t B) { return hist_shape_bytes(B, hist_shape(B)); }
 
 template <bool kGather, int kFpl, int kWarps, int kStages>
-static void launch_hist_variant(unsigned gy, cudaStream_t st, const uint8_t* bins_rm, int32_t F_pad, int32_t F,
-                                int32_t B, const uint4* qstats, const uint32_t* perm, const HistChunk* chunks,
-                                const uint32_t* n_chunks, ull* built, int64_t feat_stride, int64_t slot_stride) {
+static void launch_hist_variant(unsigned gy, unsigned gz, cudaStream_t st, const uint8_t* bins_rm, int32_t F_pad,
+                                int32_t F, int32_t B, const uint4* qstats, const uint32_t* perm,
+                                const HistChunk* chunks, const uint32_t* n_chunks, ull* built, int64_t feat_stride,
+                                int64_t slot_stride, int64_t set_qstride, int64_t set_built_stride) {
     ensure_dyn_smem((const void*)hist_kernel<kGather, kFpl, kWarps, kStages>, (int)hist_smem_bytes(B));
-    const dim3 grid((unsigned)hist_n_tiles(F, kFpl), gy);
+    const dim3 grid((unsigned)hist_n_tiles(F, kFpl), gy, gz);
     hist_kernel<kGather, kFpl, kWarps, kStages><<<grid, kWarps * 32, hist_smem_bytes(B), st>>>(
-        bins_rm, F_pad, F, B, qstats, perm, chunks, n_chunks, built, feat_stride, slot_stride);
+        bins_rm, F_pad, F, B, qstats, perm, chunks, n_chunks, built, feat_stride, slot_stride, set_qstride,
+        set_built_stride);
 }
 
 int hist_tiles(int32_t F, int32_t B) { return hist_n_tiles(F, hist_shape(B).fpl); }
+int hist_lane_features(int32_t B) { return hist_shape(B).fpl; }
+
+void launch_hist_sets(const uint8_t* bins_rm, int32_t F_pad, int32_t F, int32_t B, const uint4* qstats,
+                      const uint32_t* perm, const HistChunk* chunks, const uint32_t* n_chunks, uint32_t max_chunks,
+                      ull* built, int64_t feat_stride, int64_t slot_stride, int32_t n_sets, int64_t set_qstride,
+                      int64_t set_built_stride, cudaStream_t st) {
+    if (max_chunks == 0 || n_sets <= 0 || F <= 0) return;
+    const unsigned gy = max_chunks < 65535u ? max_chunks : 65535u;
+    const unsigned gz = (unsigned)n_sets;
+    const bool two = hist_shape(B).fpl == 2;
+#define CBGPU_HIST_ARGS gy, gz, st, bins_rm, F_pad, F, B, qstats, perm, chunks, n_chunks, built, feat_stride, \
+                        slot_stride, set_qstride, set_built_stride
+    if (perm) {
+        if (two) launch_hist_variant<true, 2, 16, 2>(CBGPU_HIST_ARGS);
+        else launch_hist_variant<true, 1, 8, 3>(CBGPU_HIST_ARGS);
+    } else {
+        if (two) launch_hist_variant<false, 2, 16, 2>(CBGPU_HIST_ARGS);
+        else launch_hist_variant<false, 1, 8, 3>(CBGPU_HIST_ARGS);
+    }
+#undef CBGPU_HIST_ARGS
+}
 
 void launch_hist(const uint8_t* bins_rm, int32_t F_pad, int32_t F, int32_t B, const uint4* qstats,
                  const uint32_t* perm, const HistChunk* chunks, const uint32_t* n_chunks, uint32_t max_chunks,
                  ull* built, int64_t feat_stride, int64_t slot_stride, cudaStream_t st) {
-    if (max_chunks == 0) return;
-    const unsigned gy = max_chunks < 65535u ? max_chunks : 65535u;
-    const bool two = hist_shape(B).fpl == 2;
-    if (perm) {
-        if (two) launch_hist_variant<true, 2, 16, 2>(gy, st, bins_rm, F_pad, F, B, qstats, perm, chunks, n_chunks, built, feat_stride, slot_stride);
-        else launch_hist_variant<true, 1, 8, 3>(gy, st, bins_rm, F_pad, F, B, qstats, perm, chunks, n_chunks, built, feat_stride, slot_stride);
-    } else {
-        if (two) launch_hist_variant<false, 2, 16, 2>(gy, st, bins_rm, F_pad, F, B, qstats, perm, chunks, n_chunks, built, feat_stride, slot_stride);
-        else launch_hist_variant<false, 1, 8, 3>(gy, st, bins_rm, F_pad, F, B, qstats, perm, chunks, n_chunks, built, feat_stride, slot_stride);
-    }
+    launch_hist_sets(bins_rm, F_pad, F, B, qstats, perm, chunks, n_chunks, max_chunks, built, feat_stride,
+                     slot_stride, 1, 0, 0, st);
 }
 
 // The level-0 work list: rows [0, n) in kChunkRows-row items (built once per

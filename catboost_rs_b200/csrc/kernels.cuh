@@ -246,11 +246,18 @@ void launch_apply(int64_t n, double* approx, const uint16_t* leaf, const double*
 // ---- per level ---------------------------------------------------------------
 void launch_zero(void* p, size_t bytes, cudaStream_t st);
 int hist_tiles(int32_t F, int32_t B);  // feature tiles (grid x) of the histogram launch
+int hist_lane_features(int32_t B);  // features each lane owns in the histogram launch (1 or 2)
 // n_chunks: device chunk count; max_chunks bounds it.  Cell (slot, f, bin, c)
 // of the output is built[slot * slot_stride + f * feat_stride + bin * 2 + c].
 void launch_hist(const uint8_t* bins_rm, int32_t F_pad, int32_t F, int32_t B, const uint4* qstats,
                  const uint32_t* perm, const HistChunk* chunks, const uint32_t* n_chunks, uint32_t max_chunks,
                  ull* built, int64_t feat_stride, int64_t slot_stride, cudaStream_t st);
+// n_sets stat sets over the same rows in one launch (grid z): set k reads
+// qstats + k * set_qstride and adds into built + k * set_built_stride.
+void launch_hist_sets(const uint8_t* bins_rm, int32_t F_pad, int32_t F, int32_t B, const uint4* qstats,
+                      const uint32_t* perm, const HistChunk* chunks, const uint32_t* n_chunks, uint32_t max_chunks,
+                      ull* built, int64_t feat_stride, int64_t slot_stride, int32_t n_sets, int64_t set_qstride,
+                      int64_t set_built_stride, cudaStream_t st);
 // The level-0 histogram work list (all rows), built once per session.
 void launch_level0_chunks(int64_t n, HistChunk* chunks, uint32_t cap, uint32_t* n_chunks, uint32_t* err,
                           cudaStream_t st);

@@ -132,12 +132,15 @@ def _assert_same_partitions(m, o, allbins, F, tol):
     assert np.max(np.abs(m.staged - o.staged)) <= tol
 
 
-@pytest.mark.parametrize("score,depth", [("Cosine", 5), ("L2", 4)])
-def test_multiclass_one_hot_matches_oracle(cb, score, depth):
+@pytest.mark.parametrize("score,depth,F,seed", [("Cosine", 5, 6, 36), ("L2", 4, 6, 35), ("Cosine", 4, 37, 72)])
+def test_multiclass_one_hot_matches_oracle(cb, score, depth, F, seed):
     # one-hot categorical features: equality candidates after the floats,
-    # first-seen perfect-hash bins, bootstrap No (upstream rejects draws)
-    rs = np.random.RandomState(31 + depth)
-    n, F, K = 20000, 6, 5
+    # first-seen perfect-hash bins, bootstrap No (upstream rejects draws).
+    # 33 float bins against up to 200 categories: the float and one-hot
+    # features take separate histogram launches (F = 37 crosses a 32-feature
+    # tile before the one-hot columns)
+    rs = np.random.RandomState(seed)
+    n, K = 20000, 5
     X = rs.standard_normal((n, F)).astype(np.float32)
     cats = _zipf_cats(rs, n, [5, 17, 60, 200])
     codes = np.array([[int(v) for v in c] for c in cats])
