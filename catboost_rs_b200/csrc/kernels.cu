@@ -1077,9 +1077,14 @@ void launch_level0_chunks(int64_t n, HistChunk* chunks, uint32_t cap, uint32_t* 
 template <int kDeriveRounds>
 __global__ void __launch_bounds__(256) derive_prefix_kernel(int level, int32_t Fs, int32_t B, const ull* __restrict__ built,
                                      const ull* __restrict__ prev, ull* __restrict__ cur,
-                                     const uint8_t* __restrict__ small_side) {
+                                     const uint8_t* __restrict__ small_side, int64_t set_built_stride,
+                                     int64_t set_cur_stride) {
     const int lane = threadIdx.x & 31;
     const int64_t row = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+    // blockIdx.y = stat set (prev and cur share a stride)
+    built += (int64_t)blockIdx.y * set_built_stride;
+    prev += (int64_t)blockIdx.y * set_cur_stride;
+    cur += (int64_t)blockIdx.y * set_cur_stride;
     const int64_t Q = 1ll << level;
     const int64_t slots = level > 0 ? Q >> 1 : 1;
     if (row >= Q * Fs) return;
@@ -1124,13 +1129,15 @@ __global__ void __launch_bounds__(256) derive_prefix_kernel(int level, int32_t F
     }
 }
 
-void launch_derive_prefix(int level, int32_t Fs, int32_t B, const ull* built, const ull* prev,
-                          ull* cur, const uint8_t* small_side, cudaStream_t st) {
+void launch_derive_prefix_sets(int level, int32_t Fs, int32_t B, const ull* built, const ull* prev, ull* cur,
+                               const uint8_t* small_side, int32_t n_sets, int64_t set_built_stride,
+                               int64_t set_cur_stride, cudaStream_t st) {
     int64_t rows = (1ll << level) * Fs;
     int64_t blocks = (rows * 32 + 255) / 256;
-    if (blocks < 1) return;
-    const unsigned g = (unsigned)blocks;
-#define CBGPU_DERIVE(K) derive_prefix_kernel<K><<<g, 256, 0, st>>>(level, Fs, B, built, prev, cur, small_side)
+    if (blocks < 1 || n_sets <= 0) return;
+    const dim3 g((unsigned)blocks, (unsigned)n_sets);
+#define CBGPU_DERIVE(K) derive_prefix_kernel<K><<<g, 256, 0, st>>>(level, Fs, B, built, prev, cur, small_side, \
+                                                                   set_built_stride, set_cur_stride)
     switch ((B + 31) / 32) {
         case 1: CBGPU_DERIVE(1); break;
         case 2: CBGPU_DERIVE(2); break;
@@ -1142,6 +1149,11 @@ void launch_derive_prefix(int level, int32_t Fs, int32_t B, const ull* built, co
         default: CBGPU_DERIVE(8); break;
     }
 #undef CBGPU_DERIVE
+}
+
+void launch_derive_prefix(int level, int32_t Fs, int32_t B, const ull* built, const ull* prev,
+                          ull* cur, const uint8_t* small_side, cudaStream_t st) {
+    launch_derive_prefix_sets(level, Fs, B, built, prev, cur, small_side, 1, 0, 0, st);
 }
 
 // ============================================================================

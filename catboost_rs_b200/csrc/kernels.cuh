@@ -271,6 +271,11 @@ void launch_level0_chunks(int64_t n, HistChunk* chunks, uint32_t cap, uint32_t* 
 // level's build-side choice).
 void launch_derive_prefix(int level, int32_t Fs, int32_t B, const ull* built, const ull* prev,
                           ull* cur, const uint8_t* small_side, cudaStream_t st);
+// n_sets stat sets in one launch (grid y): set k reads built + k *
+// set_built_stride and prev + k * set_cur_stride, writes cur + k * set_cur_stride.
+void launch_derive_prefix_sets(int level, int32_t Fs, int32_t B, const ull* built, const ull* prev, ull* cur,
+                               const uint8_t* small_side, int32_t n_sets, int64_t set_built_stride,
+                               int64_t set_cur_stride, cudaStream_t st);
 void launch_score(int level, int32_t Fs, int32_t f0, int32_t F, int32_t B, const ull* cur,
                   const int32_t* border_counts, double l2, int score_fn, double* grp_score, int32_t* grp_bin,
                   TreeState* ts, ull* rank_best, uint8_t* small_side, cudaStream_t st);

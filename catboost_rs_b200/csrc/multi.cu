@@ -1714,11 +1714,13 @@ struct cbgpu_multi_session {
     bool fast = false;
     int fast_pairs = 0, F_pad = 0;
     // When the one-hot features' values widen the table past the float
-    // features' bins, the two kinds get separate histogram launches: the float
-    // features (bins < NBf) in columns [0, F0) of bins_rm, the one-hot features
-    // from column cat_col (a multiple of 32, so each launch's row slices stay
-    // 16-byte aligned); cat_col = 0 means one launch over all F features.
-    int NBf = 0, cat_col = 0;
+    // features' bins (NBf), the histogram takes two launches over the same
+    // rows: features [0, wide_col) at NBf bins in the narrower-table shape,
+    // [wide_col, F) (the last F0 mod 32 float features, then the one-hot
+    // features, which fill a 32-lane tile's idle lanes) at NB bins.  wide_col
+    // is a multiple of 32, so both launches' row slices stay 16-byte aligned;
+    // 0 means one launch over all F features.
+    int NBf = 0, wide_col = 0;
     uint8_t* bins_rm = nullptr;            // u8 [n][F_pad]
     uint4* qpairs = nullptr;               // [fast_pairs][n] packed channel pairs
     unsigned long long* fbuilt = nullptr;  // [fast_pairs][F][slots][NB][2] built children
@@ -2037,8 +2039,8 @@ int fast_setup(cbgpu_multi_session* s) {
     int maxb = 0;
     for (int f = 0; f < F0; ++f) maxb = std::max(maxb, (int)s->bc[(size_t)f]);
     s->NBf = maxb + 1;
-    s->cat_col = F0 > 0 && F0 < F && hist_lane_features(s->NBf) > hist_lane_features(NB) ? (F0 + 31) / 32 * 32 : 0;
-    s->F_pad = s->cat_col ? s->cat_col + (F - F0 + 31) / 32 * 32 : (F + 31) / 32 * 32;
+    s->wide_col = F0 < F && hist_lane_features(s->NBf) > hist_lane_features(NB) ? F0 / 32 * 32 : 0;
+    s->F_pad = (F + 31) / 32 * 32;
     MDA(s->bins_rm, (size_t)std::max<int64_t>(n, 1) * s->F_pad);
     MDA(s->qpairs, (size_t)s->fast_pairs * std::max<int64_t>(n, 1));
     s->fbuilt_cells = (size_t)F * std::max(1, L / 4) * NB * 2;
@@ -2058,13 +2060,7 @@ int fast_setup(cbgpu_multi_session* s) {
     MDA(s->fn_chunks0, 1);
     MDA(s->fts, 1);
     MCU(cudaMemsetAsync(s->fts, 0, sizeof(TreeState), st));
-    if (n > 0 && s->cat_col) {
-        launch_transpose_fm_to_rm(s->bins_fm, n, n, F0, s->bins_rm, s->F_pad, st);
-        launch_transpose_fm_to_rm(s->bins_fm + (size_t)F0 * n, n, n, F - F0, s->bins_rm + s->cat_col, s->F_pad,
-                                  st);
-    } else if (n > 0) {
-        launch_transpose_fm_to_rm(s->bins_fm, n, n, F, s->bins_rm, s->F_pad, st);
-    }
+    if (n > 0) launch_transpose_fm_to_rm(s->bins_fm, n, n, F, s->bins_rm, s->F_pad, st);
     launch_level0_chunks(n, s->fchunks0, (uint32_t)(n / kChunkRows) + 2, s->fn_chunks0,
                          (uint32_t*)((char*)s->fts + offsetof(TreeState, err)), st);
     MCU(cudaGetLastError());
@@ -2659,20 +2655,18 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
             // fbuilt is zeroed above, so a float feature's cells past its NBf
             // bins stay 0 when only those bins are built
             // (every channel pair in one launch: grid z)
-            const int Fh = s->cat_col ? s->F0 : F;
-            launch_hist_sets(s->bins_rm, s->F_pad, Fh, s->cat_col ? s->NBf : NB, s->qpairs,
-                             l == 0 ? nullptr : s->flist, l == 0 ? s->fchunks0 : s->fchunks,
-                             l == 0 ? s->fn_chunks0 : s->fn_chunks, max_chunks, s->fbuilt, (int64_t)slots * NB * 2,
-                             (int64_t)NB * 2, P, n, (int64_t)bcells, st);
-            if (s->cat_col)
-                launch_hist_sets(s->bins_rm + s->cat_col, s->F_pad, F - Fh, NB, s->qpairs,
-                                 l == 0 ? nullptr : s->flist, l == 0 ? s->fchunks0 : s->fchunks,
-                                 l == 0 ? s->fn_chunks0 : s->fn_chunks, max_chunks,
-                                 s->fbuilt + (size_t)Fh * slots * NB * 2, (int64_t)slots * NB * 2, (int64_t)NB * 2,
-                                 P, n, (int64_t)bcells, st);
-            for (int p = 0; p < P; ++p)
-                launch_derive_prefix(l, F, NB, s->fbuilt + (size_t)p * bcells, s->fcur[cur ^ 1] + (size_t)p * s->fcur_cells,
-                                     s->fcur[cur] + (size_t)p * s->fcur_cells, s->fside, st);
+            const int Fw = s->wide_col;
+            if (Fw > 0)
+                launch_hist_sets(s->bins_rm, s->F_pad, Fw, s->NBf, s->qpairs, l == 0 ? nullptr : s->flist,
+                                 l == 0 ? s->fchunks0 : s->fchunks, l == 0 ? s->fn_chunks0 : s->fn_chunks,
+                                 max_chunks, s->fbuilt, (int64_t)slots * NB * 2, (int64_t)NB * 2, P, n,
+                                 (int64_t)bcells, st);
+            launch_hist_sets(s->bins_rm + Fw, s->F_pad, F - Fw, NB, s->qpairs, l == 0 ? nullptr : s->flist,
+                             l == 0 ? s->fchunks0 : s->fchunks, l == 0 ? s->fn_chunks0 : s->fn_chunks, max_chunks,
+                             s->fbuilt + (size_t)Fw * slots * NB * 2, (int64_t)slots * NB * 2, (int64_t)NB * 2, P,
+                             n, (int64_t)bcells, st);
+            launch_derive_prefix_sets(l, F, NB, s->fbuilt, s->fcur[cur ^ 1], s->fcur[cur], s->fside, P,
+                                      (int64_t)bcells, (int64_t)s->fcur_cells, st);
             mc_gather_kernel<<<grid_for((int64_t)Q * F * NB * C), kMcThreads, 0, st>>>(Q, F, NB, C, s->fcur[cur],
                                                                                      s->fcur_cells, s->hist);
             mc_score_kernel<<<grid_for((int64_t)F * NB), kMcThreads, 0, st>>>(Q, F, NB, K, s->hist, s->d_bc,

@@ -132,13 +132,15 @@ def _assert_same_partitions(m, o, allbins, F, tol):
     assert np.max(np.abs(m.staged - o.staged)) <= tol
 
 
-@pytest.mark.parametrize("score,depth,F,seed", [("Cosine", 5, 6, 36), ("L2", 4, 6, 35), ("Cosine", 4, 37, 72)])
+@pytest.mark.parametrize("score,depth,F,seed", [("Cosine", 5, 6, 36), ("L2", 4, 6, 35), ("Cosine", 4, 37, 72),
+                                                 ("L2", 3, 62, 73)])
 def test_multiclass_one_hot_matches_oracle(cb, score, depth, F, seed):
     # one-hot categorical features: equality candidates after the floats,
     # first-seen perfect-hash bins, bootstrap No (upstream rejects draws).
-    # 33 float bins against up to 200 categories: the float and one-hot
-    # features take separate histogram launches (F = 37 crosses a 32-feature
-    # tile before the one-hot columns)
+    # 33 float bins against up to 200 categories: past 32 float features the
+    # histogram takes two launches, the first 32 * (F // 32) float features at
+    # 33 bins and the rest with the one-hot features at 200 (F = 62: 30 + 4
+    # features overflow one 32-lane tile)
     rs = np.random.RandomState(seed)
     n, K = 20000, 5
     X = rs.standard_normal((n, F)).astype(np.float32)
