@@ -393,57 +393,94 @@ __device__ __forceinline__ double mc_avg(double s, double w, double l2) {
 // histogram.rs:1160-1290): candidate b is present[f - F0][b], its TRUE
 // children the bin's cells (prefix(b) - prefix(b - 1)), its FALSE children the
 // parent totals minus them.
-__global__ void mc_score_kernel(int parents, int F, int NB, int K, const unsigned long long* __restrict__ pre,
-                                const int32_t* __restrict__ border_counts, const McState* __restrict__ ms,
-                                double l2, int score_fn, int F0, const uint8_t* __restrict__ present,
-                                double* __restrict__ scores) {
-    const int64_t cand = (int64_t)F * NB;
+// Block = 32 consecutive borders of one feature (lane = border).  The
+// 2 K parents terms of each candidate are computed in pieces of 32 by the
+// eight compute warps (warps 1-8) into a double-buffered shared table, while
+// warp 0 adds the previous piece in order, one lane per candidate: each sum
+// sees the CPU's terms in the CPU's sequence, and the terms' loads and
+// divisions run in parallel instead of on one thread's dependent chain.
+constexpr int kMsCompute = 8;   // compute warps
+constexpr int kMsPiece = 32;    // terms per piece
+__global__ void __launch_bounds__((kMsCompute + 1) * 32)
+mc_score_kernel(int parents, int F, int NB, int K, const unsigned long long* __restrict__ pre,
+                const int32_t* __restrict__ border_counts, const McState* __restrict__ ms, double l2, int score_fn,
+                int F0, const uint8_t* __restrict__ present, double* __restrict__ scores) {
+    __shared__ double tn[2][kMsPiece][32], td[2][kMsPiece][32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int groups = (NB + 31) / 32;
+    const int f = blockIdx.x / groups;
+    const int b = (blockIdx.x % groups) * 32 + lane;
+    if (f >= F) return;
     const int C = K + 1;
     const double inv = ldexp(1.0, -ms->hist_shift);
-    for (int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < cand; k += (int64_t)gridDim.x * blockDim.x) {
-        const int f = (int)(k / NB), b = (int)(k - (int64_t)f * NB);
-        const bool cat = f >= F0;
-        if (cat ? !present[(size_t)(f - F0) * NB + b] : (b >= border_counts[f] || b >= NB - 1)) {
-            scores[k] = -INFINITY;
-            continue;
+    const bool cat = f >= F0;
+    const bool cosine = score_fn == CBGPU_SCORE_COSINE;
+    const bool valid = b < NB && (cat ? present[(size_t)(f - F0) * NB + b] != 0
+                                      : (b < border_counts[f] && b < NB - 1));
+    const int T = 2 * K * parents;  // (dimension, side, leaf) terms, leaf fastest
+    const int pieces = (T + kMsPiece - 1) / kMsPiece;
+    // terms [t0, t0 + kMsPiece) of this lane's candidate into buffer buf
+    auto compute = [&](int t0, int buf) {
+        for (int j = warp - 1; j < kMsPiece; j += kMsCompute) {
+            const int t = t0 + j;
+            double vn = 0.0, vd = 0.0;
+            if (t < T && valid) {
+                const int d = t / (2 * parents), side = (t / parents) & 1, q = t % parents;
+                const unsigned long long* row = pre + ((size_t)q * F + f) * NB * C;
+                long long wp = (long long)__ldg(row + (size_t)b * C + K);
+                const long long wt = (long long)__ldg(row + (size_t)(NB - 1) * C + K);
+                long long sp = (long long)__ldg(row + (size_t)b * C + d);
+                const long long stot = (long long)__ldg(row + (size_t)(NB - 1) * C + d);
+                double w, sv;
+                if (cat) {  // the bin's own cell: TRUE = cell, FALSE = total - cell
+                    if (b > 0) {
+                        wp -= (long long)__ldg(row + (size_t)(b - 1) * C + K);
+                        sp -= (long long)__ldg(row + (size_t)(b - 1) * C + d);
+                    }
+                    w = __dmul_rn((double)(side ? wp : wt - wp), inv);
+                    sv = __dmul_rn((double)(side ? sp : stot - sp), inv);
+                } else {
+                    w = __dmul_rn((double)(side ? wt - wp : wp), inv);
+                    sv = __dmul_rn((double)(side ? stot - sp : sp), inv);
+                }
+                if (score_fn > 1) {  // SolarL2 / LOOL2 / SatL2: per-leaf terms, no l2
+                    vn = gpu_score_term(score_fn, sv, w);
+                } else {
+                    const double avg = mc_avg(sv, w, l2);
+                    vn = __dmul_rn(avg, sv);
+                    if (cosine) vd = __dmul_rn(__dmul_rn(avg, avg), w);
+                }
+            }
+            tn[buf][j][lane] = vn;
+            td[buf][j][lane] = vd;
         }
-        // one walk over the (dimension, side, leaf) terms feeds both sums, each
-        // in the CPU's order (the numerator's and the denominator's passes see
-        // the same terms in the same sequence)
-        double num = 0.0, den = 1e-100;
-        const bool cosine = score_fn == CBGPU_SCORE_COSINE;
-        for (int d = 0; d < K; ++d) {
-            for (int side = 0; side < 2; ++side) {  // false children, then true children
-                for (int q = 0; q < parents; ++q) {
-                    const unsigned long long* row = pre + ((size_t)q * F + f) * NB * C;
-                    long long wp = (long long)row[(size_t)b * C + K];
-                    const long long wt = (long long)row[(size_t)(NB - 1) * C + K];
-                    long long sp = (long long)row[(size_t)b * C + d];
-                    const long long st = (long long)row[(size_t)(NB - 1) * C + d];
-                    double w, s;
-                    if (cat) {  // the bin's own cell: TRUE = cell, FALSE = total - cell
-                        if (b > 0) {
-                            wp -= (long long)row[(size_t)(b - 1) * C + K];
-                            sp -= (long long)row[(size_t)(b - 1) * C + d];
-                        }
-                        w = __dmul_rn((double)(side ? wp : wt - wp), inv);
-                        s = __dmul_rn((double)(side ? sp : st - sp), inv);
-                    } else {
-                        w = __dmul_rn((double)(side ? wt - wp : wp), inv);
-                        s = __dmul_rn((double)(side ? st - sp : sp), inv);
-                    }
-                    if (score_fn > 1) {  // SolarL2 / LOOL2 / SatL2: per-leaf terms, no l2
-                        num = __dadd_rn(num, gpu_score_term(score_fn, s, w));
-                        continue;
-                    }
-                    const double avg = mc_avg(s, w, l2);
-                    num = __dadd_rn(num, __dmul_rn(avg, s));
-                    if (cosine) den = __dadd_rn(den, __dmul_rn(__dmul_rn(avg, avg), w));
+    };
+    double num = 0.0, den = 1e-100;
+    if (warp > 0) compute(0, 0);
+    __syncthreads();
+    for (int pc = 0; pc < pieces; ++pc) {
+        const int buf = pc & 1;
+        if (warp > 0) {
+            if (pc + 1 < pieces) compute((pc + 1) * kMsPiece, buf ^ 1);
+        } else {
+            const int cnt = T - pc * kMsPiece < kMsPiece ? T - pc * kMsPiece : kMsPiece;
+            if (cnt == kMsPiece) {
+#pragma unroll 8
+                for (int j = 0; j < kMsPiece; ++j) {
+                    num = __dadd_rn(num, tn[buf][j][lane]);
+                    if (cosine) den = __dadd_rn(den, td[buf][j][lane]);
+                }
+            } else {
+                for (int j = 0; j < cnt; ++j) {
+                    num = __dadd_rn(num, tn[buf][j][lane]);
+                    if (cosine) den = __dadd_rn(den, td[buf][j][lane]);
                 }
             }
         }
-        scores[k] = score_fn != CBGPU_SCORE_COSINE ? num : __ddiv_rn(num, sqrt(den));
+        __syncthreads();
     }
+    if (warp == 0 && b < NB)
+        scores[(size_t)f * NB + b] = !valid ? -INFINITY : (!cosine ? num : __ddiv_rn(num, sqrt(den)));
 }
 
 // Strict first-wins argmax over (feature, border) (tree.rs:355-366): the
@@ -516,13 +553,21 @@ mc_leafsum_kernel(int64_t n, int K, int L, const double* __restrict__ approx, co
     // RMSEWithUncertainty's ders are unbounded: its sums take the tree's score
     // shift less 2 (|w der2| <= 2 |w der1_1| + 2 w <= 4 max channel)
     const int leaf_shift = diag == 2 ? ms->hist_shift - 2 : leaf_shift_in;
+    // shared table: the (lo, hi) 32-bit words of each int64 cell, lo words
+    // first (add_split64; 64-bit shared atomics would be compare-and-swap loops)
     extern __shared__ unsigned long long ltab[];
     const int pk = K * (K + 1) / 2, W = K + pk;
+    uint32_t* tlo = (uint32_t*)ltab;
+    uint32_t* thi = tlo + (size_t)L * W;
     if (use_smem) {
         for (int k = threadIdx.x; k < L * W; k += blockDim.x) ltab[k] = 0ull;
         __syncthreads();
     }
-    unsigned long long* dst = use_smem ? ltab : sums;
+    auto add = [&](size_t c, double x) {
+        const long long v = llrint(ldexp(x, leaf_shift));
+        if (use_smem) add_split64(tlo + c, thi + c, v);
+        else atomicAdd(&sums[c], (unsigned long long)v);
+    };
     double p[kMcMaxK];
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
         const int q = leaf[i];
@@ -530,41 +575,37 @@ mc_leafsum_kernel(int64_t n, int K, int L, const double* __restrict__ approx, co
             atomicOr(&ms->err, kMcErrLeafRange);
             continue;
         }
-        unsigned long long* cell = dst + (size_t)q * W;
-        for (int d = 0; d < K; ++d)
-            atomicAdd(&cell[d], (unsigned long long)llrint(ldexp(wd1[(size_t)d * n + i], leaf_shift)));
+        const size_t cell = (size_t)q * W;
+        for (int d = 0; d < K; ++d) add(cell + d, wd1[(size_t)d * n + i]);
         const double w = weight ? weight[i] : 1.0;
         if (diag == 2) {
             const double diff = __dsub_rn(tmat[i], approx[i]);
             const double prec = exp(__dmul_rn(-2.0, approx[(size_t)n + i]));
             const double dsp = __dmul_rn(__dmul_rn(diff, diff), prec);
-            atomicAdd(&cell[K], (unsigned long long)llrint(ldexp(-w, leaf_shift)));
-            atomicAdd(&cell[K + 1], (unsigned long long)llrint(ldexp(__dmul_rn(__dmul_rn(-2.0, w), dsp), leaf_shift)));
+            add(cell + K, -w);
+            add(cell + K + 1, __dmul_rn(__dmul_rn(-2.0, w), dsp));
             continue;
         }
         if (diag) {
             for (int d = 0; d < K; ++d) {
                 const double pd = mc_sigmoid(approx[(size_t)d * n + i]);
-                const double h = __dmul_rn(__dmul_rn(-pd, __dsub_rn(1.0, pd)), w);
-                atomicAdd(&cell[K + d], (unsigned long long)llrint(ldexp(h, leaf_shift)));
+                add(cell + K + d, __dmul_rn(__dmul_rn(-pd, __dsub_rn(1.0, pd)), w));
             }
             continue;
         }
         mc_softmax(approx, n, i, K, p);
         int j = 0;
         for (int dy = 0; dy < K; ++dy) {
-            const double hyy = __dmul_rn(__dmul_rn(p[dy], __dsub_rn(p[dy], 1.0)), w);
-            atomicAdd(&cell[K + j++], (unsigned long long)llrint(ldexp(hyy, leaf_shift)));
-            for (int dx = dy + 1; dx < K; ++dx) {
-                const double hyx = __dmul_rn(__dmul_rn(p[dy], p[dx]), w);
-                atomicAdd(&cell[K + j++], (unsigned long long)llrint(ldexp(hyx, leaf_shift)));
-            }
+            add(cell + K + j++, __dmul_rn(__dmul_rn(p[dy], __dsub_rn(p[dy], 1.0)), w));
+            for (int dx = dy + 1; dx < K; ++dx) add(cell + K + j++, __dmul_rn(__dmul_rn(p[dy], p[dx]), w));
         }
     }
     if (use_smem) {
         __syncthreads();
-        for (int k = threadIdx.x; k < L * W; k += blockDim.x)
-            if (ltab[k]) atomicAdd(&sums[k], ltab[k]);
+        for (int k = threadIdx.x; k < L * W; k += blockDim.x) {
+            const unsigned long long v = ((unsigned long long)thi[k] << 32) | tlo[k];
+            if (v) atomicAdd(&sums[k], v);
+        }
     }
 }
 
@@ -2669,9 +2710,8 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
                                       (int64_t)bcells, (int64_t)s->fcur_cells, st);
             mc_gather_kernel<<<grid_for((int64_t)Q * F * NB * C), kMcThreads, 0, st>>>(Q, F, NB, C, s->fcur[cur],
                                                                                      s->fcur_cells, s->hist);
-            mc_score_kernel<<<grid_for((int64_t)F * NB), kMcThreads, 0, st>>>(Q, F, NB, K, s->hist, s->d_bc,
-                                                                              s->d_ms, s->l2, s->score_fn, s->F0,
-                                                                              s->d_present, s->scores);
+            mc_score_kernel<<<(unsigned)(F * ((NB + 31) / 32)), (kMsCompute + 1) * 32, 0, st>>>(
+                Q, F, NB, K, s->hist, s->d_bc, s->d_ms, s->l2, s->score_fn, s->F0, s->d_present, s->scores);
             mc_argmax_kernel<<<1, 1024, 0, st>>>((int64_t)F * NB, NB, s->scores, l, s->d_ms);
             if (l + 1 < D) {
                 mc_side_kernel<<<1, 1024, 0, st>>>(l, F, NB, C, K, s->F0, s->hist, s->d_ms, s->fts, s->fside);
@@ -2730,9 +2770,8 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
                                   st>>>(leaves, F, NB, C, s->hist, s->d_pstat, s->d_bc, s->d_ms, s->raw_l2,
                                         s->pw_shift, pw_smem, s->d_pwscratch, s->scores);
         } else {
-            mc_score_kernel<<<grid_for((int64_t)F * NB), kMcThreads, 0, st>>>(leaves, F, NB, K, s->hist, s->d_bc,
-                                                                              s->d_ms, s->l2, s->score_fn, s->F0,
-                                                                              s->d_present, s->scores);
+            mc_score_kernel<<<(unsigned)(F * ((NB + 31) / 32)), (kMsCompute + 1) * 32, 0, st>>>(
+                leaves, F, NB, K, s->hist, s->d_bc, s->d_ms, s->l2, s->score_fn, s->F0, s->d_present, s->scores);
         }
         mc_argmax_kernel<<<1, 1024, 0, st>>>((int64_t)F * NB, NB, s->scores, l, s->d_ms);
         mc_route_kernel<<<g, kMcThreads, 0, st>>>(n, l, s->bins_fm, s->F0, s->d_ms, s->leaf);
