@@ -1244,12 +1244,14 @@ __global__ void rk_srank_kernel(int n_groups, const int64_t* __restrict__ goff, 
 // decay^k formed by k successive multiplications.  idx / boot are n-sized
 // scratch indexed by object.
 constexpr int kYetiWarps = 4;  // groups per 128-thread block
+constexpr int kYetiSmemDocs = 256;  // groups up to this size keep their sort keys in shared memory
 
 __global__ void __launch_bounds__(kYetiWarps * 32) rk_yeti_sample_kernel(
     int n_groups, const int64_t* __restrict__ goff, const double* __restrict__ ap, const double* __restrict__ target,
     int perms, const double* __restrict__ decay_pow, const uint64_t* __restrict__ seeds,
     const int64_t* __restrict__ cwoff, float* __restrict__ cw, int32_t* __restrict__ idx,
     double* __restrict__ boot) {
+    __shared__ double skey[kYetiWarps][kYetiSmemDocs];
     const int lane = threadIdx.x & 31;
     const int gi = blockIdx.x * kYetiWarps + (threadIdx.x >> 5);
     if (gi >= n_groups) return;  // warp-uniform
@@ -1259,7 +1261,7 @@ __global__ void __launch_bounds__(kYetiWarps * 32) rk_yeti_sample_kernel(
     if (g == 0) return;
     const Rng64 base = Rng64::from_seed(seeds[gi]);
     int32_t* ix = idx + b;
-    double* bt = boot + b;
+    double* bt = g <= kYetiSmemDocs ? skey[threadIdx.x >> 5] : boot + b;
     __syncwarp();
     for (int p = 0; p < perms; ++p) {
         for (int64_t i = lane; i < g; i += 32) {
@@ -1273,6 +1275,7 @@ __global__ void __launch_bounds__(kYetiWarps * 32) rk_yeti_sample_kernel(
         for (int64_t i = lane; i < g; i += 32) {
             const double key = bt[i];
             int64_t pos = 0;
+#pragma unroll 4
             for (int64_t j = 0; j < g; ++j) {
                 const double o = bt[j];
                 pos += (o > key || (o == key && j < i)) ? 1 : 0;
@@ -1315,46 +1318,53 @@ __global__ void __launch_bounds__(kYetiWarps * 32) rk_yeti_der_kernel(
     for (int64_t i = lane; i < g; i += 32) ex[b + i] = exp(ap[b + i]);
     __syncwarp();
     bool finite = true;
-    for (int64_t x = lane; x < g; x += 32) {
-        double a1 = 0.0, a2 = 0.0, ae = 0.0;
-        const double ewx = ex[b + x];
-        for (int64_t wl = 0; wl < g; ++wl) {
-            if (wl == x) {  // x as the winner: its losers in ascending order
-                double wd = 0.0, wd2 = 0.0;
-                for (int64_t ll = 0; ll < g; ++ll) {
-                    const float cv = cwg[x * g + ll];
-                    if (cv == 0.0f && qw_finite) continue;
-                    const float wf = __fdiv_rn(__fmul_rn(qw, cv), den);
-                    if (wf == 0.0f) continue;
+    // Lane x walks 2g - 1 steps: column cells (x as the loser of wl) for
+    // wl < x, then its own winner row (losers ascending, summed apart and
+    // added to der1 / der2 when the row ends), then column cells for wl > x.
+    // Every lane takes the same step count, so no lane waits on another's
+    // row, and each sum still takes its terms in the sequential loop's order.
+    for (int64_t x0 = 0; x0 < g; x0 += 32) {
+        const int64_t x = x0 + lane;
+        const bool act = x < g;
+        double a1 = 0.0, a2 = 0.0, ae = 0.0, wd = 0.0, wd2 = 0.0;
+        const double ewx = act ? ex[b + x] : 0.0;
+        for (int64_t st = 0; st < 2 * g - 1; ++st) {
+            if (!act) continue;
+            const bool row = st >= x && st < x + g;
+            const int64_t o = row ? st - x : (st < x ? st : st - g + 1);  // loser (row) or winner (column)
+            const float cv = row ? cwg[x * g + o] : cwg[o * g + x];
+            if (!(cv == 0.0f && qw_finite)) {
+                const float wf = __fdiv_rn(__fmul_rn(qw, cv), den);
+                if (wf != 0.0f) {
                     const double c = (double)wf;
-                    const double el = ex[b + ll];
-                    const double dn = __dadd_rn(el, ewx);
-                    const double p = dn > 0.0 ? __ddiv_rn(el, dn) : 0.5;
-                    const double cp = __dmul_rn(c, p);
-                    wd = __dadd_rn(wd, cp);
-                    wd2 = __dadd_rn(wd2, __dmul_rn(cp, __dsub_rn(p, 1.0)));
+                    const double eo = ex[b + o];
+                    if (row) {
+                        const double dn = __dadd_rn(eo, ewx);
+                        const double p = dn > 0.0 ? __ddiv_rn(eo, dn) : 0.5;
+                        const double cp = __dmul_rn(c, p);
+                        wd = __dadd_rn(wd, cp);
+                        wd2 = __dadd_rn(wd2, __dmul_rn(cp, __dsub_rn(p, 1.0)));
+                    } else {
+                        const double dn = __dadd_rn(ewx, eo);
+                        const double p = dn > 0.0 ? __ddiv_rn(ewx, dn) : 0.5;
+                        const double cp = __dmul_rn(c, p);
+                        a1 = __dsub_rn(a1, cp);
+                        a2 = __dadd_rn(a2, __dmul_rn(cp, __dsub_rn(p, 1.0)));
+                    }
                     ae = __dadd_rn(ae, c);
                 }
+            }
+            if (st == x + g - 1) {  // the winner row ends
                 a1 = __dadd_rn(a1, wd);
                 a2 = __dadd_rn(a2, wd2);
-                continue;
             }
-            const float cv = cwg[wl * g + x];  // x as a loser of wl
-            if (cv == 0.0f && qw_finite) continue;
-            const float wf = __fdiv_rn(__fmul_rn(qw, cv), den);
-            if (wf == 0.0f) continue;
-            const double c = (double)wf;
-            const double dn = __dadd_rn(ewx, ex[b + wl]);
-            const double p = dn > 0.0 ? __ddiv_rn(ewx, dn) : 0.5;
-            const double cp = __dmul_rn(c, p);
-            a1 = __dsub_rn(a1, cp);
-            a2 = __dadd_rn(a2, __dmul_rn(cp, __dsub_rn(p, 1.0)));
-            ae = __dadd_rn(ae, c);
         }
-        d1[b + x] = a1;
-        d2[b + x] = a2;
-        if (eff) eff[b + x] = ae;
-        finite &= isfinite(a1) && isfinite(a2);
+        if (act) {
+            d1[b + x] = a1;
+            d2[b + x] = a2;
+            if (eff) eff[b + x] = ae;
+            finite &= isfinite(a1) && isfinite(a2);
+        }
     }
     if (__any_sync(0xffffffffu, !finite) && lane == 0) atomicOr(&ms->err, kMcErrNonFinite);
 }
