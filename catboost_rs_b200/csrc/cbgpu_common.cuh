@@ -22,11 +22,13 @@ CBGPU_HD uint32_t pcg_mix(uint64_t x) {
     return (xs >> rot) | (xs << ((32u - rot) & 31u));
 }
 
-// O(log delta) jump of one LCG stream (rng.rs:45-69).
-CBGPU_HD uint64_t lcg_advance(uint64_t seed, uint64_t c, uint64_t delta) {
+// The multiplier pair of an O(log delta) jump of an LCG stream (rng.rs:45-69):
+// delta steps take x to x * apow + c * adiv, for any increment c.
+CBGPU_HD void lcg_jump(uint64_t delta, uint64_t& apow, uint64_t& adiv) {
     uint64_t mask = 1;
     while (mask != (1ULL << 63) && (mask << 1) <= delta) mask <<= 1;
-    uint64_t apow = 1, adiv = 0;
+    apow = 1;
+    adiv = 0;
     while (mask != 0) {
         adiv = adiv * (apow + 1);
         apow = apow * apow;
@@ -36,6 +38,11 @@ CBGPU_HD uint64_t lcg_advance(uint64_t seed, uint64_t c, uint64_t delta) {
         }
         mask >>= 1;
     }
+}
+
+CBGPU_HD uint64_t lcg_advance(uint64_t seed, uint64_t c, uint64_t delta) {
+    uint64_t apow, adiv;
+    lcg_jump(delta, apow, adiv);
     return seed * apow + c * adiv;
 }
 
@@ -78,6 +85,11 @@ struct Rng64 {
     CBGPU_HD void advance(uint64_t d) {
         x1 = lcg_advance(x1, c1, d);
         x2 = lcg_advance(x2, c2, d);
+    }
+    // a jump by a fixed distance whose (apow, adiv) pair is known (lcg_jump)
+    CBGPU_HD void jump(uint64_t apow, uint64_t adiv) {
+        x1 = x1 * apow + c1 * adiv;
+        x2 = x2 * apow + c2 * adiv;
     }
 };
 

@@ -1246,22 +1246,105 @@ __global__ void rk_srank_kernel(int n_groups, const int64_t* __restrict__ goff, 
 constexpr int kYetiWarps = 4;  // groups per 128-thread block
 constexpr int kYetiSmemDocs = 256;  // groups up to this size keep their sort keys in shared memory
 
+// The sampler for a group of g <= 32 * kSlots documents with its keys, exps,
+// order and relevances in shared memory: each lane keeps the RNG states of its
+// documents' first draw and moves them by fixed jumps (32 documents within a
+// permutation, g between permutations), and counts the ranks of its kSlots
+// documents in one pass over the keys.
+template <int kSlots>
+__device__ __forceinline__ void yeti_sample_smem(int64_t g, int lane, const Rng64& base, int perms,
+                                                 const double* __restrict__ apg, const double* __restrict__ tg,
+                                                 const double* __restrict__ decay_pow, float* __restrict__ cwg,
+                                                 double* __restrict__ key, double* __restrict__ ex,
+                                                 int32_t* __restrict__ ix, float* __restrict__ rel) {
+    for (int64_t i = lane; i < g; i += 32) {
+        ex[i] = exp(apg[i]);
+        rel[i] = __double2float_rn(tg[i]);
+    }
+    uint64_t a32, d32, ag, dg;
+    lcg_jump(32, a32, d32);
+    lcg_jump((uint64_t)g, ag, dg);
+    Rng64 first = base;  // draw (permutation p, document lane)
+    first.advance((uint64_t)lane);
+    __syncwarp();
+    for (int p = 0; p < perms; ++p) {
+        double k[kSlots];
+        Rng64 r = first;
+#pragma unroll
+        for (int sl = 0; sl < kSlots; ++sl) {
+            const int64_t i = lane + 32 * sl;
+            Rng64 d = r;
+            const float u = __double2float_rn(real1(d));
+            const float ratio = __fdiv_rn(u, __fsub_rn(1.000001f, u));
+            k[sl] = i < g ? __dmul_rn(ex[i], (double)ratio) : 0.0;
+            if (i < g) key[i] = k[sl];
+            r.jump(a32, d32);
+        }
+        first.jump(ag, dg);
+        __syncwarp();
+        // position of i = documents with a larger key, or an equal key and a
+        // smaller index (the stable descending order)
+        int pos[kSlots];
+#pragma unroll
+        for (int sl = 0; sl < kSlots; ++sl) pos[sl] = 0;
+        for (int64_t j = 0; j < g; ++j) {
+            const double o = key[j];
+#pragma unroll
+            for (int sl = 0; sl < kSlots; ++sl)
+                pos[sl] += (o > k[sl] || (o == k[sl] && j < lane + 32 * sl)) ? 1 : 0;
+        }
+#pragma unroll
+        for (int sl = 0; sl < kSlots; ++sl)
+            if (lane + 32 * sl < g) ix[pos[sl]] = lane + 32 * sl;
+        __syncwarp();
+        for (int64_t d = 1 + lane; d < g; d += 32) {
+            const int32_t fi = ix[d - 1], se = ix[d];
+            const float rf = rel[fi], rs = rel[se];
+            const float pw =
+                __double2float_rn(__dmul_rn(__dmul_rn(0.15, decay_pow[d - 1]), (double)fabsf(__fsub_rn(rf, rs))));
+            if (rf > rs) cwg[fi * g + se] = __fadd_rn(cwg[fi * g + se], pw);
+            else if (rf < rs) cwg[se * g + fi] = __fadd_rn(cwg[se * g + fi], pw);
+        }
+        __syncwarp();
+    }
+}
+
 __global__ void __launch_bounds__(kYetiWarps * 32) rk_yeti_sample_kernel(
     int n_groups, const int64_t* __restrict__ goff, const double* __restrict__ ap, const double* __restrict__ target,
     int perms, const double* __restrict__ decay_pow, const uint64_t* __restrict__ seeds,
     const int64_t* __restrict__ cwoff, float* __restrict__ cw, int32_t* __restrict__ idx,
     double* __restrict__ boot) {
-    __shared__ double skey[kYetiWarps][kYetiSmemDocs];
-    const int lane = threadIdx.x & 31;
-    const int gi = blockIdx.x * kYetiWarps + (threadIdx.x >> 5);
+    __shared__ double skey[kYetiWarps][kYetiSmemDocs], sex[kYetiWarps][kYetiSmemDocs];
+    __shared__ int32_t six[kYetiWarps][kYetiSmemDocs];
+    __shared__ float srel[kYetiWarps][kYetiSmemDocs];
+    const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
+    const int gi = blockIdx.x * kYetiWarps + wp;
     if (gi >= n_groups) return;  // warp-uniform
     const int64_t b = goff[gi], g = goff[gi + 1] - b;
     float* cwg = cw + cwoff[gi];
     for (int64_t k = lane; k < g * g; k += 32) cwg[k] = 0.0f;
     if (g == 0) return;
     const Rng64 base = Rng64::from_seed(seeds[gi]);
+    if (g <= kYetiSmemDocs) {
+        __syncwarp();
+#define CBGPU_YS(S) yeti_sample_smem<S>(g, lane, base, perms, ap + b, target + b, decay_pow, cwg, skey[wp], \
+                                        sex[wp], six[wp], srel[wp])
+        switch ((g + 31) / 32) {
+            case 1: CBGPU_YS(1); break;
+            case 2: CBGPU_YS(2); break;
+            case 3: CBGPU_YS(3); break;
+            case 4: CBGPU_YS(4); break;
+            case 5: CBGPU_YS(5); break;
+            case 6: CBGPU_YS(6); break;
+            case 7: CBGPU_YS(7); break;
+            default: CBGPU_YS(8); break;
+        }
+#undef CBGPU_YS
+        return;
+    }
+    // larger groups: keys and order in the n-sized scratch
     int32_t* ix = idx + b;
-    double* bt = g <= kYetiSmemDocs ? skey[threadIdx.x >> 5] : boot + b;
+    double* bt = boot + b;
     __syncwarp();
     for (int p = 0; p < perms; ++p) {
         for (int64_t i = lane; i < g; i += 32) {
@@ -1295,6 +1378,126 @@ __global__ void __launch_bounds__(kYetiWarps * 32) rk_yeti_sample_kernel(
     }
 }
 
+// One pair cell's contribution, shared by both walks: the pair weight
+// wf = qw * cv / perms (f32) and the loser's probability p = e_l / (e_l + e_w);
+// returns false for a skipped cell (wf == 0).
+__device__ __forceinline__ bool yeti_cell(float cv, float qw, float den, double el, double ew, double& c,
+                                          double& cp, double& q) {
+    const float wf = __fdiv_rn(__fmul_rn(qw, cv), den);
+    if (wf == 0.0f) return false;
+    c = (double)wf;
+    const double dn = __dadd_rn(el, ew);
+    const double p = dn > 0.0 ? __ddiv_rn(el, dn) : 0.5;
+    cp = __dmul_rn(c, p);
+    q = __dmul_rn(cp, __dsub_rn(p, 1.0));
+    return true;
+}
+
+constexpr int kYetiMaskDocs = 128;  // groups up to this size take the sparse walk
+constexpr int kYetiMaskWords = kYetiMaskDocs / 32;
+
+// The sparse walk for a group of g <= kYetiMaskDocs documents with a finite
+// weight (where zero cells are skipped): non-zero masks of the pair matrix are
+// built from coalesced row reads (row masks in shared memory, each lane's
+// column masks in registers), then lane x visits only its non-zero cells, in
+// the dense walk's order: winners w < x of its column, its own row's losers,
+// winners w > x.  The sums are the dense walk's, term for term.
+__device__ __forceinline__ void yeti_der_sparse(int64_t g, const float* __restrict__ cwg,
+                                                const double* __restrict__ exg, float qw, float den,
+                                                uint32_t* __restrict__ rmask, double* __restrict__ d1,
+                                                double* __restrict__ d2, double* __restrict__ eff, int lane,
+                                                bool& finite) {
+    const int W = (int)((g + 31) >> 5);
+    uint32_t cmask[kYetiMaskWords][kYetiMaskWords];  // [column slot][row word]
+#pragma unroll
+    for (int k = 0; k < kYetiMaskWords; ++k)
+#pragma unroll
+        for (int w = 0; w < kYetiMaskWords; ++w) cmask[k][w] = 0u;
+    // rows in batches of 4 whose loads issue before their ballots
+    constexpr int kRowBatch = 4;
+#pragma unroll
+    for (int rw = 0; rw < kYetiMaskWords; ++rw) {
+        if (rw >= W) break;
+        for (int ri0 = 0; ri0 < 32 && rw * 32 + ri0 < g; ri0 += kRowBatch) {
+            float v[kRowBatch][kYetiMaskWords];
+#pragma unroll
+            for (int j = 0; j < kRowBatch; ++j) {
+                const int64_t r = rw * 32 + ri0 + j;
+#pragma unroll
+                for (int k = 0; k < kYetiMaskWords; ++k) {
+                    const int64_t c = lane + 32 * k;
+                    v[j][k] = (k < W && r < g && c < g) ? cwg[r * g + c] : 0.0f;
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < kRowBatch; ++j) {
+                const int64_t r = rw * 32 + ri0 + j;
+                if (r >= g) break;
+#pragma unroll
+                for (int k = 0; k < kYetiMaskWords; ++k) {
+                    if (k >= W) break;
+                    const bool nz = v[j][k] != 0.0f;
+                    const uint32_t bal = __ballot_sync(0xffffffffu, nz);
+                    if (lane == 0) rmask[r * kYetiMaskWords + k] = bal;
+                    cmask[k][rw] |= (nz ? 1u : 0u) << (ri0 + j);
+                }
+            }
+        }
+    }
+    __syncwarp();
+#pragma unroll
+    for (int k = 0; k < kYetiMaskWords; ++k) {
+        if (k >= W) break;
+        const int64_t x = lane + 32 * k;
+        if (x < g) {
+            const double ewx = exg[x];
+            double a1 = 0.0, a2 = 0.0, ae = 0.0, wd = 0.0, wd2 = 0.0, c, cp, q;
+            // winners of column x: below x, then (after the row) above x
+            auto column = [&](bool above) {
+#pragma unroll
+                for (int rw = 0; rw < kYetiMaskWords; ++rw) {
+                    uint32_t m = cmask[k][rw];
+                    const int lo = rw * 32;
+                    // bits w < x (or w > x) of this word
+                    const int64_t cut = x - lo;  // bit index of x in this word
+                    if (!above) m = cut <= 0 ? 0u : (cut >= 32 ? m : m & ((1u << cut) - 1u));
+                    else m = cut < 0 ? m : (cut >= 31 ? 0u : m & ~((2u << cut) - 1u));
+                    while (m) {
+                        const int w = lo + __ffs(m) - 1;
+                        m &= m - 1;
+                        if (yeti_cell(cwg[(int64_t)w * g + x], qw, den, ewx, exg[w], c, cp, q)) {
+                            a1 = __dsub_rn(a1, cp);
+                            a2 = __dadd_rn(a2, q);
+                            ae = __dadd_rn(ae, c);
+                        }
+                    }
+                }
+            };
+            column(false);
+#pragma unroll
+            for (int lw = 0; lw < kYetiMaskWords; ++lw) {
+                uint32_t m = lw < W ? rmask[x * kYetiMaskWords + lw] : 0u;
+                while (m) {
+                    const int l = lw * 32 + __ffs(m) - 1;
+                    m &= m - 1;
+                    if (yeti_cell(cwg[x * g + l], qw, den, exg[l], ewx, c, cp, q)) {
+                        wd = __dadd_rn(wd, cp);
+                        wd2 = __dadd_rn(wd2, q);
+                        ae = __dadd_rn(ae, c);
+                    }
+                }
+            }
+            a1 = __dadd_rn(a1, wd);
+            a2 = __dadd_rn(a2, wd2);
+            column(true);
+            d1[x] = a1;
+            d2[x] = a2;
+            if (eff) eff[x] = ae;
+            finite &= isfinite(a1) && isfinite(a2);
+        }
+    }
+}
+
 // The PairLogit der over one phase's sampled pairs (pairlogit_group_der,
 // ranking_der.rs:400-440), winner rows ascending, losers ascending, pair
 // weight (qw * cw / perms) in f32; eff (when given) gets the pairwise weights
@@ -1307,6 +1510,7 @@ __global__ void __launch_bounds__(kYetiWarps * 32) rk_yeti_der_kernel(
     int n_groups, const int64_t* __restrict__ goff, const double* __restrict__ ap, const double* __restrict__ gw,
     int perms, const int64_t* __restrict__ cwoff, const float* __restrict__ cw, double* __restrict__ d1,
     double* __restrict__ d2, double* __restrict__ eff, double* __restrict__ ex, McState* __restrict__ ms) {
+    __shared__ uint32_t s_rmask[kYetiWarps][kYetiMaskDocs * kYetiMaskWords];
     const int lane = threadIdx.x & 31;
     const int gi = blockIdx.x * kYetiWarps + (threadIdx.x >> 5);
     if (gi >= n_groups) return;  // warp-uniform
@@ -1318,6 +1522,12 @@ __global__ void __launch_bounds__(kYetiWarps * 32) rk_yeti_der_kernel(
     for (int64_t i = lane; i < g; i += 32) ex[b + i] = exp(ap[b + i]);
     __syncwarp();
     bool finite = true;
+    if (qw_finite && g <= kYetiMaskDocs) {
+        yeti_der_sparse(g, cwg, ex + b, qw, den, s_rmask[threadIdx.x >> 5], d1 + b, d2 + b, eff ? eff + b : nullptr,
+                        lane, finite);
+        if (__any_sync(0xffffffffu, !finite) && lane == 0) atomicOr(&ms->err, kMcErrNonFinite);
+        return;
+    }
     // Lane x walks 2g - 1 steps: column cells (x as the loser of wl) for
     // wl < x, then its own winner row (losers ascending, summed apart and
     // added to der1 / der2 when the row ends), then column cells for wl > x.
