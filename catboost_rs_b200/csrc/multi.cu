@@ -885,6 +885,59 @@ __global__ void rk_der_kernel(int n_groups, int mode, const int64_t* __restrict_
     if (!finite) atomicOr(&ms->err, kMcErrNonFinite);
 }
 
+constexpr int kYetiWarps = 4;  // groups per 128-thread block (warp-per-group ranking kernels)
+
+// PairLogit derivatives with one warp per group and one lane per document
+// (the PairLogit arm of rk_der_kernel, ranking_der.rs:400-440, restated per
+// document).  The sequential loop visits winners in ascending order and each
+// winner's competitors in input order: a document's der1 / der2 receive, in
+// that order, -p (and p (p - 1)) for each pair it loses to a winner at or
+// below its own index -- its own self pairs included, as they come while its
+// competitor list runs -- then its own list's sums, then the pairs it loses to
+// later winners.  Its loser slots (lstart / lpair, ascending slot index) are
+// that order, so each lane's sums round exactly as the loop's.
+__global__ void __launch_bounds__(kYetiWarps * 32) rk_pairlogit_der_kernel(
+    int n_groups, const int64_t* __restrict__ goff, const int64_t* __restrict__ cstart,
+    const int64_t* __restrict__ closer, const int64_t* __restrict__ pwin, const int64_t* __restrict__ lstart,
+    const int64_t* __restrict__ lpair, const double* __restrict__ approx, double* __restrict__ ex,
+    double* __restrict__ d1, double* __restrict__ d2, McState* __restrict__ ms) {
+    const int lane = threadIdx.x & 31;
+    const int gi = blockIdx.x * kYetiWarps + (threadIdx.x >> 5);
+    if (gi >= n_groups) return;  // warp-uniform
+    const int64_t b = goff[gi], e = goff[gi + 1];
+    for (int64_t i = b + lane; i < e; i += 32) ex[i] = exp(approx[i]);
+    __syncwarp();
+    bool finite = true;
+    for (int64_t x = b + lane; x < e; x += 32) {
+        const double exx = ex[x];
+        double a1 = 0.0, a2 = 0.0;
+        auto lose = [&](int64_t k) {  // x loses pair k: p = e^x / (e^x + e^winner)
+            const double den = __dadd_rn(exx, ex[pwin[k]]);
+            const double p = den > 0.0 ? __ddiv_rn(exx, den) : 0.5;
+            a1 = __dsub_rn(a1, __dmul_rn(1.0, p));
+            a2 = __dadd_rn(a2, __dmul_rn(__dmul_rn(1.0, p), __dsub_rn(p, 1.0)));
+        };
+        int64_t j = lstart[x];
+        const int64_t je = lstart[x + 1];
+        for (; j < je && pwin[lpair[j]] <= x; ++j) lose(lpair[j]);
+        double wd = 0.0, wd2 = 0.0;
+        for (int64_t k = cstart[x]; k < cstart[x + 1]; ++k) {
+            const double el = ex[closer[k]];
+            const double den = __dadd_rn(el, exx);
+            const double p = den > 0.0 ? __ddiv_rn(el, den) : 0.5;
+            wd = __dadd_rn(wd, __dmul_rn(1.0, p));
+            wd2 = __dadd_rn(wd2, __dmul_rn(__dmul_rn(1.0, p), __dsub_rn(p, 1.0)));
+        }
+        a1 = __dadd_rn(a1, wd);
+        a2 = __dadd_rn(a2, wd2);
+        for (; j < je; ++j) lose(lpair[j]);
+        d1[x] = a1;
+        d2[x] = a2;
+        finite &= isfinite(a1) && isfinite(a2);
+    }
+    if (__any_sync(0xffffffffu, !finite) && lane == 0) atomicOr(&ms->err, kMcErrNonFinite);
+}
+
 // Ranking-mode leaf sums: per leaf the sums of der1, der2 (unit leaf weights
 // for Newton, boosting.rs:8345-8380) -- or, for Gradient leaves (count = 1),
 // the row count -- and of the object weight (normalize_leaf_values' leaf
@@ -1019,7 +1072,24 @@ __global__ void __launch_bounds__(kLsThreads) rk_leafsum_runs_kernel(int L, cons
         if (at + kC < m) stage(at + kC, buf ^ 1);  // the next chunk, while thread 0 adds this one
         if (threadIdx.x == 0) {
             const uint32_t cnt = m - at < (uint32_t)kC ? m - at : (uint32_t)kC;
-            for (uint32_t k = 0; k < cnt; ++k) {
+            uint32_t k = 0;
+            // 8 values' loads issue ahead of their (ordered) additions
+            for (; k + 8 <= cnt; k += 8) {
+                double x1[8], x2[8], x3[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    x1[u] = c1[buf][k + u];
+                    x2[u] = c2[buf][k + u];
+                    x3[u] = c3[buf][k + u];
+                }
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    s1 = __dadd_rn(s1, x1[u]);
+                    s2 = __dadd_rn(s2, x2[u]);
+                    s3 = __dadd_rn(s3, x3[u]);
+                }
+            }
+            for (; k < cnt; ++k) {
                 s1 = __dadd_rn(s1, c1[buf][k]);
                 s2 = __dadd_rn(s2, c2[buf][k]);
                 s3 = __dadd_rn(s3, c3[buf][k]);
@@ -1243,7 +1313,6 @@ __global__ void rk_srank_kernel(int n_groups, const int64_t* __restrict__ goff, 
 // other in order -- every rounding is the sequential loop's.  decay_pow[k] =
 // decay^k formed by k successive multiplications.  idx / boot are n-sized
 // scratch indexed by object.
-constexpr int kYetiWarps = 4;  // groups per 128-thread block
 constexpr int kYetiSmemDocs = 256;  // groups up to this size keep their sort keys in shared memory
 
 // The sampler for a group of g <= 32 * kSlots documents with its keys, exps,
@@ -2002,6 +2071,10 @@ struct cbgpu_multi_session {
     // the level's pair statistics, the leaf pair-weight matrix, scratch
     int64_t n_pairs = 0;
     int64_t* d_pwin = nullptr;
+    // PairLogit: each document's loser slots (competitor indices k with
+    // closer[k] == doc, ascending), their offsets, exp(approx) scratch
+    int64_t *d_lstart = nullptr, *d_lpair = nullptr;
+    double* d_pex = nullptr;
     long long *d_pstat = nullptr, *d_pwsum = nullptr;
     int pw_shift = 0;  // pair weights in the statistics: llrint(w * 2^pw_shift)
     double* d_pwscratch = nullptr;
@@ -2059,6 +2132,9 @@ struct cbgpu_multi_session {
         cudaFree(d_lmideal);
         cudaFree(d_lmorder);
         cudaFree(d_pwin);
+        cudaFree(d_lstart);
+        cudaFree(d_lpair);
+        cudaFree(d_pex);
         cudaFree(d_pstat);
         cudaFree(d_pwsum);
         cudaFree(d_pwscratch);
@@ -2517,7 +2593,7 @@ int cbgpu_rank_begin_raw(const cbgpu_begin_args* a, const int64_t* group_offsets
     // (calc_pairwise_weights, boosting.rs:1761-1780)
     std::vector<int64_t> cstart((size_t)n + 1, 0), closer((size_t)std::max<int64_t>(n_pairs, 1));
     std::vector<double> eff((size_t)n, 0.0);
-    std::vector<int64_t> win;
+    std::vector<int64_t> win, lstart, lpair;
     if (mode == kRankPairLogit || mode == kRankPairLogitPairwise) {
         for (int64_t k = 0; k < n_pairs; ++k) {
             const int64_t wv = pair_winner[k], lv = pair_loser[k];
@@ -2538,6 +2614,15 @@ int cbgpu_rank_begin_raw(const cbgpu_begin_args* a, const int64_t* group_offsets
                     eff[(size_t)wi] += 1.0;
                     eff[(size_t)closer[(size_t)k]] += 1.0;
                 }
+        if (mode == kRankPairLogit) {
+            // loser slots by document, ascending k: by winner, then input order
+            lstart.assign((size_t)n + 1, 0);
+            lpair.assign(closer.size(), 0);
+            for (int64_t k = 0; k < n_pairs; ++k) lstart[(size_t)closer[(size_t)k] + 1]++;
+            for (int64_t i = 0; i < n; ++i) lstart[(size_t)i + 1] += lstart[(size_t)i];
+            std::vector<int64_t> lfill(lstart.begin(), lstart.end() - 1);
+            for (int64_t k = 0; k < n_pairs; ++k) lpair[(size_t)lfill[(size_t)closer[(size_t)k]]++] = k;
+        }
     } else {
         for (int64_t i = 0; i < n; ++i) eff[(size_t)i] = a->weight ? a->weight[i] : 1.0;
     }
@@ -2570,6 +2655,13 @@ int cbgpu_rank_begin_raw(const cbgpu_begin_args* a, const int64_t* group_offsets
         if (!rc) rc = mdalloc(&s->d_eff, (size_t)n);
         if (!rc) rc = mdalloc(&s->d_der2, (size_t)n);
         if (!rc) rc = mdalloc(&s->d_tgt, (size_t)n);
+        if (!rc && mode == kRankPairLogit) {
+            s->n_pairs = n_pairs;
+            rc = mdalloc(&s->d_pwin, win.size());
+            if (!rc) rc = mdalloc(&s->d_lstart, lstart.size());
+            if (!rc) rc = mdalloc(&s->d_lpair, lpair.size());
+            if (!rc) rc = mdalloc(&s->d_pex, (size_t)std::max<int64_t>(n, 1));
+        }
         if (!rc && (mode == kRankYetiRank || mode == kRankYetiRankPairwise)) {
             // group weight: the mean member weight (query_info.rs:180-187)
             std::vector<double> gw((size_t)n_groups);
@@ -2662,6 +2754,10 @@ int cbgpu_rank_begin_raw(const cbgpu_begin_args* a, const int64_t* group_offsets
         if (e == cudaSuccess) e = cudaMemcpy(s->d_eff, eff.data(), sizeof(double) * (size_t)n, cudaMemcpyHostToDevice);
         if (e == cudaSuccess && s->d_pwin)
             e = cudaMemcpy(s->d_pwin, win.data(), sizeof(int64_t) * win.size(), cudaMemcpyHostToDevice);
+        if (e == cudaSuccess && s->d_lstart)
+            e = cudaMemcpy(s->d_lstart, lstart.data(), sizeof(int64_t) * lstart.size(), cudaMemcpyHostToDevice);
+        if (e == cudaSuccess && s->d_lpair)
+            e = cudaMemcpy(s->d_lpair, lpair.data(), sizeof(int64_t) * lpair.size(), cudaMemcpyHostToDevice);
         if (e != cudaSuccess) rc = mfail(CBGPU_ERR_CUDA, "rank_begin: upload failed: %s", cudaGetErrorString(e));
     }
     if (rc) {
@@ -2873,6 +2969,10 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
         rk_srank_kernel<<<yg, 128, 0, st>>>(s->n_groups, s->d_goff, s->approx, s->d_tgt, s->srank_ndcg, s->srank_sigma,
                                            s->srank_mu, s->srank_num_est, srank_base[0], s->d_lmden, s->d_lmideal,
                                            s->d_srank_ws, s->d_lmorder, s->wd1, s->d_der2, s->d_ms);
+    } else if (s->rank_mode == kRankPairLogit) {
+        rk_pairlogit_der_kernel<<<yw, kYetiWarps * 32, 0, st>>>(s->n_groups, s->d_goff, s->d_cstart, s->d_closer,
+                                                                s->d_pwin, s->d_lstart, s->d_lpair, s->approx,
+                                                                s->d_pex, s->wd1, s->d_der2, s->d_ms);
     } else if (s->rank_mode >= 0) {
         rk_der_kernel<<<(unsigned)((s->n_groups + 127) / 128), 128, 0, st>>>(
             s->n_groups, s->rank_mode, s->d_goff, s->d_cstart, s->d_closer, s->approx, s->d_tgt, s->weight,
