@@ -288,9 +288,13 @@ __device__ __forceinline__ double mvs_der_obj(double wd) { return sqrt(__dmul_rn
 __global__ void __launch_bounds__(kMvsThreads) mvs_threshold_kernel(
     int64_t n, const double* __restrict__ wd1, const TreeParams* __restrict__ tp, double rate,
     double* __restrict__ thresholds) {
+    // the block's values stay in place (val); the recursion partitions 16-bit
+    // indices between two buffers (96 KB in all: two blocks per SM, so one
+    // block's sequential sum overlaps the other's partition)
     extern __shared__ double msm[];
-    double* bufA = msm;
-    double* bufB = msm + kMvsBlock;
+    double* val = msm;
+    uint16_t* bufA = (uint16_t*)(msm + kMvsBlock);
+    uint16_t* bufB = bufA + kMvsBlock;
     __shared__ int s_scan[40];
     __shared__ double s_state[4];  // sum_small_cur, n_large_cur, result
     __shared__ int s_ctl[4];       // len, which buffer/offset, done
@@ -300,7 +304,8 @@ __global__ void __launch_bounds__(kMvsThreads) mvs_threshold_kernel(
     const int bs = (int)(end - beg);
     for (int k = threadIdx.x; k < bs; k += blockDim.x) {
         double d = mvs_der_obj(wd1[beg + k]);
-        bufA[k] = sqrt(__dadd_rn(lambda, __dmul_rn(d, d)));
+        val[k] = sqrt(__dadd_rn(lambda, __dmul_rn(d, d)));
+        bufA[k] = (uint16_t)k;
     }
     const double sample_size = (double)__fmul_rn((float)rate, (float)bs);
     if (threadIdx.x == 0) {
@@ -313,19 +318,19 @@ __global__ void __launch_bounds__(kMvsThreads) mvs_threshold_kernel(
     __syncthreads();
     for (;;) {
         const int len = s_ctl[0];
-        double* cur = (s_ctl[1] & 1 ? bufB : bufA) + (s_ctl[1] >> 1);
-        double* oth = (s_ctl[1] & 1) ? bufA : bufB;
+        const uint16_t* cur = (s_ctl[1] & 1 ? bufB : bufA) + (s_ctl[1] >> 1);
+        uint16_t* oth = (s_ctl[1] & 1) ? bufA : bufB;
         if (len == 0) {
             if (threadIdx.x == 0) thresholds[blockIdx.x] = 0.0;
             return;
         }
-        const double thr = cur[0];
+        const double thr = val[cur[0]];
         const int per = (len + blockDim.x - 1) / blockDim.x;
         const int k0 = threadIdx.x * per;
         const int k1 = k0 + per < len ? k0 + per : len;
         int cs = 0, cm = 0, cl = 0;
         for (int k = k0; k < k1; ++k) {
-            double c = cur[k];
+            double c = val[cur[k]];
             if (c < thr) ++cs; else if (c <= thr) ++cm; else ++cl;
         }
         int ts, tl;
@@ -335,14 +340,23 @@ __global__ void __launch_bounds__(kMvsThreads) mvs_threshold_kernel(
         (void)block_excl_scan<int>(cm, s_scan, &tm_dummy);
         const int tm = tm_dummy;
         for (int k = k0; k < k1; ++k) {
-            double c = cur[k];
-            if (c < thr) oth[ps++] = c;
-            else if (!(c <= thr)) oth[ts + pl++] = c;
+            const uint16_t ik = cur[k];
+            double c = val[ik];
+            if (c < thr) oth[ps++] = ik;
+            else if (!(c <= thr)) oth[ts + pl++] = ik;
         }
         __syncthreads();
         if (threadIdx.x == 0) {
             double sum_small_upd = 0.0;
-            for (int k = 0; k < ts; ++k) sum_small_upd = __dadd_rn(sum_small_upd, oth[k]);
+            int k = 0;
+            for (; k + 8 <= ts; k += 8) {  // 8 loads ahead of their (ordered) additions
+                double x[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) x[u] = val[oth[k + u]];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) sum_small_upd = __dadd_rn(sum_small_upd, x[u]);
+            }
+            for (; k < ts; ++k) sum_small_upd = __dadd_rn(sum_small_upd, val[oth[k]]);
             const double s_cur = s_state[0], nl_cur = s_state[1];
             const double nl_upd = (double)tl, n_mid = (double)tm;
             const double sum_mid = __dmul_rn(n_mid, thr);
@@ -430,7 +444,8 @@ void launch_mvs(int64_t n, int64_t row_offset, const double* wd1, const TreePara
                 double* thresholds, float* out_sw, cudaStream_t st) {
     int64_t blocks = (n + kMvsBlock - 1) / kMvsBlock;
     if (blocks < 1) return;
-    size_t smem = sizeof(double) * 2 * kMvsBlock;
+    size_t smem = sizeof(double) * kMvsBlock + 2 * sizeof(uint16_t) * kMvsBlock;
+    static_assert(kMvsBlock <= 65536, "16-bit indices");
     ensure_dyn_smem((const void*)mvs_threshold_kernel, (int)smem);
     mvs_threshold_kernel<<<(unsigned)blocks, kMvsThreads, smem, st>>>(n, wd1, tp, rate, thresholds);
     mvs_weights_kernel<<<(unsigned)blocks, kMvsThreads, 0, st>>>(n, row_offset, wd1, tp, thresholds, out_sw);
