@@ -40,7 +40,8 @@ class BeginArgs(C.Structure):
 
 
 EXPORTS = [
-    "cbgpu_begin", "cbgpu_begin_raw", "cbgpu_grow_tree", "cbgpu_end", "cbgpu_compute_gradients",
+    "cbgpu_begin", "cbgpu_begin_raw", "cbgpu_grow_tree", "cbgpu_end", "cbgpu_stage_sample",
+    "cbgpu_compute_gradients",
     "cbgpu_last_error", "cbgpu_session_approx", "cbgpu_session_bins", "cbgpu_session_last_sample",
     "cbgpu_session_timing", "cbgpu_session_timing_sum", "cbgpu_session_set_profiling", "cbgpu_session_set_graphs", "cbgpu_session_rng_state",
     "cbgpu_histogram", "cbgpu_bootstrap_weights", "cbgpu_nccl_unique_id", "cbgpu_version",
@@ -76,6 +77,7 @@ def load(path: str = LIB_PATH):
         "cbgpu_begin_raw": ([C.POINTER(BeginArgs), vp, vp, vp, C.POINTER(vp)], C.c_int),
         "cbgpu_grow_tree": ([vp, vp, vp, i64, vp, i64, vp, vp, vp, vp, vp, i32], C.c_int),
         "cbgpu_end": ([vp], C.c_int),
+        "cbgpu_stage_sample": ([vp, vp, i64], C.c_int),
         "cbgpu_compute_gradients": ([i32, vp, vp, i64, vp, vp], C.c_int),
         "cbgpu_last_error": ([], C.c_char_p),
         "cbgpu_session_approx": ([vp, vp, i64], C.c_int),

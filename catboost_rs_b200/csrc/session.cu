@@ -130,6 +130,12 @@ struct cbgpu_session {
     // configuration
     int device = 0;
     int loss = 0, depth = 0, score_fn = 0, boot = 0, sample_from_host = 0;
+    // staged host samples (cbgpu_stage_sample): a FIFO of two device buffers
+    // filled on copy_st; a grow call without a sample takes the oldest
+    cudaStream_t copy_st = nullptr;
+    double* stage_buf[2] = {nullptr, nullptr};
+    cudaEvent_t stage_done[2] = {nullptr, nullptr}, stage_free[2] = {nullptr, nullptr};
+    int stage_head = 0, stage_count = 0;
     // Exact leaves (MAE / Quantile): quantile_der1's alpha / delta, sort buffers
     int exact = 0;
     double q_alpha = 0.5, q_delta = 1e-6;
@@ -399,6 +405,7 @@ void free_session(cbgpu_session* s) {
         s->comm = nullptr;
     }
     if (s->st) cudaStreamSynchronize(s->st);
+    if (s->copy_st) cudaStreamSynchronize(s->copy_st);  // staged copies still read the caller's buffers
     // graphs hold NCCL work: released before the communicator
     for (auto& g : s->graph)
         if (g) cudaGraphExecDestroy(g);
@@ -418,7 +425,13 @@ void free_session(cbgpu_session* s) {
             if (e) cudaEventDestroy(e);
     for (auto& e : s->uev)
         if (e) cudaEventDestroy(e);
+    for (int k = 0; k < 2; ++k) {
+        if (s->stage_buf[k]) cudaFree(s->stage_buf[k]);
+        if (s->stage_done[k]) cudaEventDestroy(s->stage_done[k]);
+        if (s->stage_free[k]) cudaEventDestroy(s->stage_free[k]);
+    }
     if (s->comm) ncclCommDestroy(s->comm);
+    if (s->copy_st) cudaStreamDestroy(s->copy_st);
     if (s->st) cudaStreamDestroy(s->st);
     delete s;
 }
@@ -713,7 +726,8 @@ int grow(cbgpu_session* s, const double* approx_h, const double* target_h, int64
          int32_t* n_splits, double* leaf_values, void* leaf_of, int32_t leaf_of_bytes) {
     if (n != s->n) return fail(CBGPU_ERR_INVALID, "LengthMismatch: n=%lld, session has %lld",
                                (long long)n, (long long)s->n);
-    // sample validation (session.rs:2405-2428)
+    // sample validation (session.rs:2405-2428); a staged sample stands in
+    // for a passed one
     if (sample_len != 0) {
         if (!s->sample_from_host)
             return fail(CBGPU_ERR_INVALID,
@@ -723,10 +737,13 @@ int grow(cbgpu_session* s, const double* approx_h, const double* target_h, int64
             return fail(CBGPU_ERR_INVALID, "LengthMismatch: sample has %lld elements, expected %lld",
                         (long long)sample_len, (long long)s->n);
         if (!sample) return fail(CBGPU_ERR_INVALID, "null sample pointer");
-    } else if (s->sample_from_host) {
+        if (s->stage_count > 0)
+            return fail(CBGPU_ERR_INVALID, "a sample was passed while %d staged sample(s) wait: pass none to "
+                                           "take the oldest staged one", s->stage_count);
+    } else if (s->sample_from_host && s->stage_count == 0) {
         return fail(CBGPU_ERR_INVALID,
                     "Degenerate: the session was opened with sample_from_host = true but no sample "
-                    "was passed");
+                    "was passed or staged");
     }
     if (!s->target_ready && !target_h) return fail(CBGPU_ERR_INVALID, "target required on the first grow");
     if (leaf_of && leaf_of_bytes) {
@@ -755,7 +772,17 @@ int grow(cbgpu_session* s, const double* approx_h, const double* target_h, int64
     tp = TreeParams{};
     int s_mode = 0, boot_mode = 0;
     bool mvs = false;
-    if (s->sample_from_host) {
+    if (s->sample_from_host && sample_len == 0) {
+        // the oldest staged sample: wait for its upload, move it into the
+        // buffer the tree reads, and free its slot for the next stage call
+        const int k = s->stage_head;
+        CU(cudaStreamWaitEvent(st, s->stage_done[k], 0));
+        CU(cudaMemcpyAsync(s->sw64, s->stage_buf[k], sizeof(double) * s->n, cudaMemcpyDeviceToDevice, st));
+        CU(cudaEventRecord(s->stage_free[k], st));
+        s->stage_head ^= 1;
+        --s->stage_count;
+        s_mode = 2;
+    } else if (s->sample_from_host) {
         CU(cudaMemcpyAsync(s->sw64, sample, sizeof(double) * s->n, cudaMemcpyHostToDevice, st));
         s_mode = 2;
     } else if (s->boot != CBGPU_BOOT_NO) {
@@ -984,6 +1011,36 @@ int cbgpu_grow_tree(cbgpu_session* s, const double* approx, const double* target
 
 int cbgpu_end(cbgpu_session* s) {
     free_session(s);
+    return CBGPU_OK;
+}
+
+int cbgpu_stage_sample(cbgpu_session* s, const double* sample, int64_t sample_len) {
+    if (!s) return fail(CBGPU_ERR_INVALID, "null session");
+    if (!s->sample_from_host)
+        return fail(CBGPU_ERR_INVALID, "Degenerate: staging a host sample needs a session opened with "
+                                       "sample_from_host = true");
+    if (sample_len != s->n)
+        return fail(CBGPU_ERR_INVALID, "LengthMismatch: sample has %lld elements, expected %lld",
+                    (long long)sample_len, (long long)s->n);
+    if (!sample) return fail(CBGPU_ERR_INVALID, "null sample pointer");
+    if (s->stage_count >= 2)
+        return fail(CBGPU_ERR_INVALID, "two staged samples already wait for their grow calls");
+    CU(cudaSetDevice(s->device));
+    if (!s->copy_st) {
+        CU(cudaStreamCreateWithFlags(&s->copy_st, cudaStreamNonBlocking));
+        for (int k = 0; k < 2; ++k) {
+            CU(cudaMalloc(&s->stage_buf[k], sizeof(double) * std::max<int64_t>(s->n, 1)));
+            CU(cudaEventCreateWithFlags(&s->stage_done[k], cudaEventDisableTiming));
+            CU(cudaEventCreateWithFlags(&s->stage_free[k], cudaEventDisableTiming));
+        }
+    }
+    const int k = (s->stage_head + s->stage_count) & 1;
+    // the slot's previous sample was moved out by a grow call on the session
+    // stream (an event never recorded is already complete)
+    CU(cudaStreamWaitEvent(s->copy_st, s->stage_free[k], 0));
+    CU(cudaMemcpyAsync(s->stage_buf[k], sample, sizeof(double) * s->n, cudaMemcpyHostToDevice, s->copy_st));
+    CU(cudaEventRecord(s->stage_done[k], s->copy_st));
+    ++s->stage_count;
     return CBGPU_OK;
 }
 

@@ -95,6 +95,7 @@ class B200Runtime:
     def __init__(self):
         self._L = _lib.load()
         self._s = C.c_void_p(None)
+        self._staged = []  # host samples whose uploads (cbgpu_stage_sample) wait for their trees
         self.n = 0
         self.depth = 0
         self.decline_reason = ""
@@ -227,16 +228,32 @@ class B200Runtime:
         rc = self._L.cbgpu_grow_tree(self._s, _ptr(a), _ptr(t), self.n, _ptr(s),
                                      0 if s is None else s.size, _ptr(sf), _ptr(sb), _ptr(ns), _ptr(lv),
                                      _ptr(lo), leaf_of_bytes if lo is not None else 0)
+        if rc == 0 and s is None and self._staged:
+            self._staged.pop(0)  # the tree took (and finished with) the oldest staged sample
         _lib.check(rc)
         k = int(ns[0])
         return DeviceGrownTree(splits=[(int(sf[i]), int(sb[i]), False) for i in range(k)],
                                leaf_values=lv,
                                leaf_of=lo if lo is not None else np.zeros(0, dtype=np.uint32))
 
+    def stage_sample(self, sample) -> None:
+        """Start uploading the host bootstrap sample of a later grow call
+        (cbgpu_stage_sample): a grow_tree_on_device call with no sample takes
+        the oldest staged one, so staging tree t + 1's sample before growing
+        tree t overlaps its upload with tree t's device work.  The array is
+        kept alive here until its tree has grown; pinned memory overlaps."""
+        if not self._s:
+            raise _lib.CbGpuError(_lib.ERR_INVALID, "no session")
+        arr = sample if (isinstance(sample, np.ndarray) and sample.dtype == np.float64
+                         and sample.flags.c_contiguous) else np.ascontiguousarray(sample, dtype=np.float64)
+        _lib.check(self._L.cbgpu_stage_sample(self._s, _ptr(arr), arr.size))
+        self._staged.append(arr)
+
     def end_device_training(self) -> None:
         if self._s:
             self._L.cbgpu_end(self._s)
             self._s = C.c_void_p(None)
+        self._staged = []
 
     def __del__(self):
         try:

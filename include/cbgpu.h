@@ -150,7 +150,8 @@ CBGPU_API int cbgpu_begin_raw(const cbgpu_begin_args* args, const float* const* 
  *  target  [n] uploaded on the first call only;
  *  sample  [sample_len] per-object bootstrap multiplier (control ? w : 0);
  *          sample_len must be n when the session was opened with
- *          sample_from_host, else 0 (session.rs:2405-2428);
+ *          sample_from_host, else 0 (session.rs:2405-2428); NULL / 0 on a
+ *          sample_from_host session takes the oldest cbgpu_stage_sample;
  * Outputs (DeviceGrownTree, runtime.rs:989-1059):
  *  split_feature / split_bin  [depth] feature and border index per level
  *          (level l is leaf bit l); the split passes iff bin > split_bin;
@@ -162,6 +163,19 @@ CBGPU_API int cbgpu_grow_tree(cbgpu_session* s, const double* approx, const doub
                     const double* sample, int64_t sample_len, int32_t* split_feature,
                     int32_t* split_bin, int32_t* n_splits, double* leaf_values, void* leaf_of,
                     int32_t leaf_of_bytes);
+
+/* Upload a host bootstrap sample ahead of the grow call that uses it.  The
+ * copy runs on a session-owned copy stream and this call returns at once; a
+ * later cbgpu_grow_tree on this session with sample = NULL, sample_len = 0
+ * takes the oldest staged sample (at most two wait at a time).  Calling
+ * stage(t + 1) before grow(t) overlaps tree t + 1's upload with tree t's
+ * device work.  The caller keeps `sample` unchanged until the grow call that
+ * takes it returns; pinned (page-locked) memory is needed for the copy to
+ * overlap.  Only for sessions opened with sample_from_host; a grow call that
+ * passes a sample while staged ones wait is an error.  No counterpart in the
+ * reference: Runtime::grow_tree_on_device (runtime.rs:1629) takes the sample
+ * with the call, which this splits in two. */
+CBGPU_API int cbgpu_stage_sample(cbgpu_session* s, const double* sample, int64_t sample_len);
 
 /* Runtime::end_device_training (runtime.rs:1648): frees the session. */
 CBGPU_API int cbgpu_end(cbgpu_session* s);

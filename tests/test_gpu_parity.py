@@ -275,6 +275,63 @@ def test_host_sample_path_matches_oracle_bootstrap():
     rt.end_device_training()
 
 
+def test_staged_host_samples_match_oracle_bootstrap():
+    """cbgpu_stage_sample: the same host-drawn samples, each staged one tree
+    ahead (stage(t + 1) before grow(t), two waiting at the start), grow the
+    oracle's trees; the staging rules are enforced."""
+    X, y, borders = make_dataset(5000, 10, seed=4, border_count=32)
+    n = X.shape[0]
+    T = 5
+    fp = cb.FitParams(loss="RMSE", depth=4, iterations=T, score_function="L2", bootstrap_type="Bernoulli",
+                      subsample=0.7, random_seed=8)
+    o = _oracle_fit(X, y, borders, fp)
+    bias = cb.starting_approx(fp, y)
+    rng = oracle.TFastRng64(8)
+    samples = []
+    for _ in range(T):
+        rng.gen_rand(); rng.gen_rand()  # PRE_TREE_DRAWS
+        sw, ctl = oracle.bootstrap("Bernoulli", np.zeros(n), rng, subsample=0.7)
+        samples.append(np.where(ctl, sw, 0.0))
+        for _ in range(4):  # replay_grow_draws + POST (device_draw_replay.rs)
+            for _ in range(X.shape[1]):
+                rng.gen_rand_real1()
+            rng.gen_rand()
+            for _ in range(X.shape[1]):
+                rng.std_normal()
+        rng.gen_rand(); rng.gen_rand()
+    rt = cb.B200Runtime()
+    cfg = cb.DeviceTrainConfig(bootstrap_type="Bernoulli", sample_rate=0.7, rng_seed=8, bias=bias,
+                               sample_from_host=True)
+    assert rt.begin_device_training_raw("RMSE", 4, True, 1, "L2", _cols(X), borders, None, n, X.shape[1],
+                                        max(len(b) for b in borders) + 1, 0.1, 3.0, cfg)
+    with pytest.raises(cb.CbGpuError, match="LengthMismatch"):
+        rt.stage_sample(np.ones(n - 1))
+    rt.stage_sample(samples[0])
+    rt.stage_sample(samples[1])
+    with pytest.raises(cb.CbGpuError, match="two staged samples"):
+        rt.stage_sample(samples[2])
+    with pytest.raises(cb.CbGpuError, match="staged sample"):  # a passed sample while staged ones wait
+        rt.grow_tree_on_device(None, y, samples[0], resident_approx=True)
+    approx = np.full(n, bias)
+    for it in range(T):
+        if 0 < it < T - 1:
+            rt.stage_sample(samples[it + 1])
+        tree = rt.grow_tree_on_device(None, y, None, resident_approx=True)
+        assert [s[0] for s in tree.splits] == list(o.split_feature[it])
+        assert [s[1] for s in tree.splits] == list(o.split_bin[it])
+        approx = approx + (tree.leaf_values * 0.1)[tree.leaf_of]
+        assert np.max(np.abs(approx - o.staged[it])) <= PRED_TOL
+    with pytest.raises(cb.CbGpuError, match="no sample was passed or staged"):
+        rt.grow_tree_on_device(None, y, None, resident_approx=True)
+    rt.end_device_training()
+    rt2 = cb.B200Runtime()
+    assert rt2.begin_device_training_raw("RMSE", 4, True, 1, "L2", _cols(X), borders, None, n, X.shape[1],
+                                         max(len(b) for b in borders) + 1, 0.1, 3.0, cb.DeviceTrainConfig())
+    with pytest.raises(cb.CbGpuError, match="sample_from_host"):
+        rt2.stage_sample(samples[0])
+    rt2.end_device_training()
+
+
 def test_seam_validation_errors():
     X, y, borders = make_dataset(300, 3, seed=1, border_count=8)
     nb = max(len(b) for b in borders) + 1
