@@ -72,3 +72,12 @@ def test_loss_ids_match_the_header():
     for name, v in runtime.LOSS.items():
         assert by_name.get(norm(name)) == v, name
     assert set(ids.values()) <= set(runtime.LOSS.values())
+
+
+def test_staging_rejects_a_null_session_on_the_host(lib):
+    # argument checks run before any CUDA call
+    lib.cbgpu_stage_sample.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64]
+    lib.cbgpu_stage_sample.restype = ctypes.c_int
+    lib.cbgpu_last_error.restype = ctypes.c_char_p
+    assert lib.cbgpu_stage_sample(None, None, 0) == 2  # CBGPU_ERR_INVALID
+    assert b"null session" in lib.cbgpu_last_error()
