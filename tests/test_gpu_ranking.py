@@ -138,6 +138,58 @@ def test_lambdamart_matches_oracle(cb, top, norm, sigma):
     assert np.max(np.abs(m.staged - o.staged)) <= TOL
 
 
+def _ranking_data_sizes(sizes, F, seed, self_pair=False):
+    # _ranking_data with given group sizes; pairs include repeats, and with
+    # self_pair one document is its own competitor
+    rs = np.random.RandomState(seed)
+    offsets = np.concatenate([[0], np.cumsum(sizes)]).astype(np.int64)
+    n = int(offsets[-1])
+    X = rs.standard_normal((n, F)).astype(np.float32)
+    score = X[:, :3] @ np.array([1.0, -0.5, 0.25]) + 0.5 * rs.standard_normal(n)
+    y = np.zeros(n)
+    pairs = []
+    for g in range(len(sizes)):
+        b, e = offsets[g], offsets[g + 1]
+        q = np.quantile(score[b:e], [0.25, 0.5, 0.75])
+        y[b:e] = np.digitize(score[b:e], q)
+        for _ in range(2 * (e - b)):
+            i, j = rs.randint(b, e, 2)
+            if y[i] > y[j]:
+                pairs.append((i, j))
+            elif y[j] > y[i]:
+                pairs.append((j, i))
+    if self_pair:
+        pairs.insert(len(pairs) // 2, (int(offsets[1]) + 3, int(offsets[1]) + 3))
+    return X, y, offsets, np.array(pairs, dtype=np.int64)
+
+
+# Group sizes on both sides of the device kernels' per-group paths: the
+# YetiRank derivative walks only the non-zero cells up to 128 documents and
+# the dense matrix beyond; its sampler keeps a group in shared memory up to
+# 256 documents (one to eight 32-document slots per lane) and in global
+# scratch beyond.
+BIG_GROUPS = [60, 140, 250, 300, 90, 200, 129, 257, 128, 33]
+
+
+@pytest.mark.parametrize("loss", ["YetiRank", "YetiRankPairwise", "PairLogit"])
+def test_large_groups_match_oracle(cb, loss):
+    X, y, offsets, pairs = _ranking_data_sizes(BIG_GROUPS, 6, 91, self_pair=(loss == "PairLogit"))
+    n, F = X.shape
+    borders = [oracle.select_borders(X[:, f], 32) for f in range(F)]
+    kw = dict(yeti_permutations=4, yeti_decay=0.85) if loss.startswith("YetiRank") else {}
+    fp = cb.FitParams(loss=loss, depth=4, iterations=3, learning_rate=0.3, l2_leaf_reg=1.0, random_seed=5,
+                      boost_from_average=False, **kw)
+    prs = pairs if loss == "PairLogit" else None
+    m = cb.fit_ranking([X[:, f].copy() for f in range(F)], borders, y, offsets, fp, pairs=prs, staged=True)
+    bins = oracle.quantize(X.T.copy(), borders)
+    o = oracle.train_ranking(bins, [len(b) for b in borders], y, offsets, loss=loss, pairs=prs, depth=4,
+                             iterations=3, learning_rate=0.3, l2_leaf_reg=1.0, random_seed=5, **kw)
+    np.testing.assert_array_equal(m.split_feature, o.split_feature)
+    np.testing.assert_array_equal(m.split_bin, o.split_bin)
+    assert np.max(np.abs(m.raw_leaf_values - o.raw_leaf_values)) <= TOL
+    assert np.max(np.abs(m.staged - o.staged)) <= TOL
+
+
 @pytest.mark.parametrize("perms,decay,weighted", [(10, 0.85, False), (3, 0.5, True)])
 def test_yetirank_matches_oracle(cb, perms, decay, weighted):
     # pairs resampled on the device every tree from the host seeder's query seeds;
