@@ -1057,11 +1057,10 @@ void launch_hist(const uint8_t* bins_rm, int32_t F_pad, int32_t F, int32_t B, co
                      slot_stride, 1, 0, 0, st);
 }
 
-// The level-0 work list: rows [0, n) in kChunkRows-row items (built once per
+// The level-0 work list: rows [0, n) in cr-row items (cr <= kChunkRows; built once per
 // session: the row count does not change).
 __global__ void level0_chunks_kernel(int64_t n, HistChunk* __restrict__ chunks, uint32_t cap,
-                                     uint32_t* __restrict__ n_chunks, uint32_t* __restrict__ err) {
-    const uint32_t cr = kChunkRows;
+                                     uint32_t* __restrict__ n_chunks, uint32_t* __restrict__ err, uint32_t cr) {
     uint32_t nch = (uint32_t)((n + cr - 1) / cr);
     if (nch > cap) {  // cannot happen with the session's sizing; never write past the buffer
         if (threadIdx.x == 0) atomicOr(err, kErrChunkCap);
@@ -1075,8 +1074,21 @@ __global__ void level0_chunks_kernel(int64_t n, HistChunk* __restrict__ chunks, 
 }
 
 void launch_level0_chunks(int64_t n, HistChunk* chunks, uint32_t cap, uint32_t* n_chunks, uint32_t* err,
-                          cudaStream_t st) {
-    level0_chunks_kernel<<<1, 1024, 0, st>>>(n, chunks, cap, n_chunks, err);
+                          uint32_t chunk_rows, cudaStream_t st) {
+    if (chunk_rows == 0 || chunk_rows > (uint32_t)kChunkRows) chunk_rows = kChunkRows;
+    level0_chunks_kernel<<<1, 1024, 0, st>>>(n, chunks, cap, n_chunks, err, chunk_rows);
+}
+
+uint32_t hist_chunk_rows(int64_t n, int tiles, int sets, int sms) {
+    // kChunkRows, or half of it when the level-0 launch would give fewer than
+    // 8 blocks per SM: small shards with few stat sets otherwise leave the
+    // last of a few waves of one-block-per-SM launches mostly empty (measured:
+    // 1M rows x 136 features, 406 -> 454 trees/s); smaller items cost more in
+    // table flushes than they gain (a quarter: 5% slower at 1.25M x 200)
+    const int64_t want = 8ll * (sms > 0 ? sms : 148);
+    uint32_t cr = kChunkRows;
+    if ((n / cr) * (int64_t)tiles * (sets > 0 ? sets : 1) < want) cr >>= 1;
+    return cr;
 }
 
 // ============================================================================
@@ -1676,7 +1688,7 @@ __global__ void __launch_bounds__(kRouteThreads, 6) partition_kernel(int level, 
 // One block, after the partition of split `level` (Q = 2^level parents):
 // parent q's built child holds cursor[q] - base[q] listed rows (rows_in null:
 // one parent of n rows; base_in null: base 0).  Writes the next level's
-// histogram work list (each built segment cut into kChunkRows-row items, in
+// histogram work list (each built segment cut into cr-row items, cr <= kChunkRows, in
 // parent order, cap items at most) and ts->hist_rows[level + 1]; when rows_out
 // is not null, the 2Q children's row counts (child q + side * Q) with their
 // segments (exclusive prefix in child order) as rows_out / base_out, and
@@ -1689,13 +1701,13 @@ __global__ void __launch_bounds__(1024) segments_kernel(int level, int64_t n, co
                                                         const uint8_t* __restrict__ small_side,
                                                         uint32_t* __restrict__ rows_out, uint32_t* __restrict__ base_out,
                                                         uint32_t* __restrict__ cursor_out, HistChunk* __restrict__ chunks,
-                                                        uint32_t cap, uint32_t* __restrict__ n_chunks, TreeState* ts) {
+                                                        uint32_t cap, uint32_t* __restrict__ n_chunks, TreeState* ts,
+                                                        uint32_t cr) {
     __shared__ uint32_t s_scan[40];
     __shared__ uint32_t s_first[kSegItemSmem];  // first work item of each parent
     const uint32_t Q = 1u << level;
     const uint32_t per = (Q + blockDim.x - 1) / blockDim.x;
     const uint32_t q0 = threadIdx.x * per;
-    const uint32_t cr = kChunkRows;
     auto base_of = [&](uint32_t q) { return base_in ? base_in[q] : 0u; };
     uint32_t rows = 0, items = 0;
     for (uint32_t q = q0; q < q0 + per && q < Q; ++q) {
@@ -1781,9 +1793,11 @@ void launch_partition(int level, int64_t n, const uint8_t* bins_fm, int64_t n_st
 
 void launch_segments(int level, int64_t n, const uint32_t* rows_in, const uint32_t* base_in, const uint32_t* cursor,
                      const uint8_t* small_side, uint32_t* rows_out, uint32_t* base_out, uint32_t* cursor_out,
-                     HistChunk* chunks, uint32_t cap, uint32_t* n_chunks, TreeState* ts, cudaStream_t st) {
+                     HistChunk* chunks, uint32_t cap, uint32_t* n_chunks, TreeState* ts, uint32_t chunk_rows,
+                     cudaStream_t st) {
+    if (chunk_rows == 0 || chunk_rows > (uint32_t)kChunkRows) chunk_rows = kChunkRows;
     segments_kernel<<<1, 1024, 0, st>>>(level, n, rows_in, base_in, cursor, small_side, rows_out, base_out,
-                                        cursor_out, chunks, cap, n_chunks, ts);
+                                        cursor_out, chunks, cap, n_chunks, ts, chunk_rows);
 }
 
 // ============================================================================

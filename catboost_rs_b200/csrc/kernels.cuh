@@ -260,7 +260,12 @@ void launch_hist_sets(const uint8_t* bins_rm, int32_t F_pad, int32_t F, int32_t 
                       int64_t set_built_stride, cudaStream_t st);
 // The level-0 histogram work list (all rows), built once per session.
 void launch_level0_chunks(int64_t n, HistChunk* chunks, uint32_t cap, uint32_t* n_chunks, uint32_t* err,
-                          cudaStream_t st);
+                          uint32_t chunk_rows, cudaStream_t st);
+// Rows per histogram work item for a session of n rows whose level-0 launch
+// has `tiles` feature tiles and `sets` stat sets on a device of `sms` SMs:
+// kChunkRows, or kChunkRows / 2 when the launch would fill fewer than 8
+// blocks per SM.  The sums do not depend on it.
+uint32_t hist_chunk_rows(int64_t n, int tiles, int sets, int sms);
 // Derive and score work on this rank's feature slice [f0, f0 + Fs) in
 // feature-major layouts (see derive_prefix_kernel).  With rank_best null the
 // winner goes to ts->split[level] and, with small_side not null, each leaf's
@@ -297,7 +302,8 @@ void launch_partition(int level, int64_t n, const uint8_t* bins_fm, int64_t n_st
 // rows_in / base_in null: level 0's single parent of n rows at base 0.
 void launch_segments(int level, int64_t n, const uint32_t* rows_in, const uint32_t* base_in, const uint32_t* cursor,
                      const uint8_t* small_side, uint32_t* rows_out, uint32_t* base_out, uint32_t* cursor_out,
-                     HistChunk* chunks, uint32_t cap, uint32_t* n_chunks, TreeState* ts, cudaStream_t st);
+                     HistChunk* chunks, uint32_t cap, uint32_t* n_chunks, TreeState* ts, uint32_t chunk_rows,
+                     cudaStream_t st);
 // The last split (`level`): leaf[i] |= (bin > border) << level, and the exact
 // int64 sums of the unsampled w * der1 and w per final leaf added into
 // leaf_sums[2 << level][2].

@@ -2051,6 +2051,7 @@ struct cbgpu_multi_session {
     // is a multiple of 32, so both launches' row slices stay 16-byte aligned;
     // 0 means one launch over all F features.
     int NBf = 0, wide_col = 0;
+    uint32_t chunk_rows = kChunkRows;  // rows per histogram work item (hist_chunk_rows)
     uint8_t* bins_rm = nullptr;            // u8 [n][F_pad]
     uint4* qpairs = nullptr;               // [fast_pairs][n] packed channel pairs
     unsigned long long* fbuilt = nullptr;  // [fast_pairs][F][slots][NB][2] built children
@@ -2378,6 +2379,12 @@ int fast_setup(cbgpu_multi_session* s) {
     s->NBf = maxb + 1;
     s->wide_col = F0 < F && hist_lane_features(s->NBf) > hist_lane_features(NB) ? F0 / 32 * 32 : 0;
     s->F_pad = (F + 31) / 32 * 32;
+    {
+        int sms = 0;
+        MCU(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, s->device));
+        const int tiles = (s->wide_col ? hist_tiles(s->wide_col, s->NBf) : 0) + hist_tiles(F - s->wide_col, NB);
+        s->chunk_rows = hist_chunk_rows(n, tiles, s->fast_pairs, sms);
+    }
     MDA(s->bins_rm, (size_t)std::max<int64_t>(n, 1) * s->F_pad);
     MDA(s->qpairs, (size_t)s->fast_pairs * std::max<int64_t>(n, 1));
     s->fbuilt_cells = (size_t)F * std::max(1, L / 4) * NB * 2;
@@ -2390,16 +2397,16 @@ int fast_setup(cbgpu_multi_session* s) {
     MDA(s->fseg_rows, 2 * kSegMax);
     MDA(s->fseg_base, 2 * kSegMax);
     MDA(s->fside, kSegMax);
-    s->fchunk_cap = (size_t)(n / kChunkRows) + (L / 2) + 2;
+    s->fchunk_cap = (size_t)(n / s->chunk_rows) + (L / 2) + 2;
     MDA(s->fchunks, s->fchunk_cap);
     MDA(s->fn_chunks, 1);
-    MDA(s->fchunks0, (size_t)(n / kChunkRows) + 2);
+    MDA(s->fchunks0, (size_t)(n / s->chunk_rows) + 2);
     MDA(s->fn_chunks0, 1);
     MDA(s->fts, 1);
     MCU(cudaMemsetAsync(s->fts, 0, sizeof(TreeState), st));
     if (n > 0) launch_transpose_fm_to_rm(s->bins_fm, n, n, F, s->bins_rm, s->F_pad, st);
-    launch_level0_chunks(n, s->fchunks0, (uint32_t)(n / kChunkRows) + 2, s->fn_chunks0,
-                         (uint32_t*)((char*)s->fts + offsetof(TreeState, err)), st);
+    launch_level0_chunks(n, s->fchunks0, (uint32_t)(n / s->chunk_rows) + 2, s->fn_chunks0,
+                         (uint32_t*)((char*)s->fts + offsetof(TreeState, err)), s->chunk_rows, st);
     MCU(cudaGetLastError());
     MCU(cudaStreamSynchronize(st));
     s->fast = true;
@@ -3012,7 +3019,7 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
             const size_t slots = l == 0 ? 1 : (size_t)Q / 2;
             const size_t bcells = (size_t)F * slots * NB * 2;
             MCU(cudaMemsetAsync(s->fbuilt, 0, sizeof(unsigned long long) * s->fbuilt_cells * P, st));
-            const uint32_t max_chunks = (uint32_t)(n / kChunkRows + slots + 1);
+            const uint32_t max_chunks = (uint32_t)(n / s->chunk_rows + slots + 1);
             // fbuilt is zeroed above, so a float feature's cells past its NBf
             // bins stay 0 when only those bins are built
             // (every channel pair in one launch: grid z)
@@ -3045,7 +3052,7 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
                                 more ? s->fseg_rows + (size_t)np * kSegMax : nullptr,
                                 more ? s->fseg_base + (size_t)np * kSegMax : nullptr,
                                 more ? s->fcursor + (size_t)np * kSegMax : nullptr, s->fchunks,
-                                (uint32_t)s->fchunk_cap, s->fn_chunks, s->fts, st);
+                                (uint32_t)s->fchunk_cap, s->fn_chunks, s->fts, s->chunk_rows, st);
             } else {
                 mc_route_kernel<<<g, kMcThreads, 0, st>>>(n, l, s->bins_fm, s->F0, s->d_ms, s->leaf);
             }

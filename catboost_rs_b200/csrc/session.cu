@@ -182,6 +182,7 @@ struct cbgpu_session {
     HistChunk* chunks0 = nullptr;  // level-0 work list (all rows), built at begin
     uint32_t* n_chunks0 = nullptr;
     HistChunk* chunks = nullptr;   // the next level's work list, built by launch_segments
+    uint32_t chunk_rows = kChunkRows;  // rows per histogram work item (hist_chunk_rows)
     size_t chunk_cap = 0;
     uint32_t* n_chunks = nullptr;
     ull* built = nullptr;
@@ -338,10 +339,15 @@ int alloc_session(cbgpu_session* s, const cbgpu_begin_args* a) {
     DA(s->small_side, kSegMax);
     DA(s->jump, 2 * kJumpSteps);
     // full chunks plus one partial chunk per segment
-    s->chunk_cap = (size_t)(n / kChunkRows) + (L / 2) + 2;
+    {
+        int sms = 0;
+        CU(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, s->device));
+        s->chunk_rows = hist_chunk_rows(n, hist_tiles(s->F, s->B), 1, sms);
+    }
+    s->chunk_cap = (size_t)(n / s->chunk_rows) + (L / 2) + 2;
     DA(s->chunks, s->chunk_cap);
     DA(s->n_chunks, 1);
-    DA(s->chunks0, (size_t)(n / kChunkRows) + 2);
+    DA(s->chunks0, (size_t)(n / s->chunk_rows) + 2);
     DA(s->n_chunks0, 1);
     feature_slice(s->F, s->world, s->rank, &s->f0, &s->Fs);
     s->built_cells = (size_t)(L / 2 > 0 ? L / 2 : 1) * s->world * s->Fs * s->B * 2;
@@ -448,7 +454,8 @@ int finish_begin(cbgpu_session* s) {
                        cudaMemcpyHostToDevice, s->st));
     if (s->n > 0) launch_transpose_fm_to_rm(s->bins_fm, s->n, s->n_stride, s->F, s->bins_rm, s->F_pad, s->st);
     launch_jump_table(s->jump, s->st);
-    launch_level0_chunks(s->n, s->chunks0, (uint32_t)(s->n / kChunkRows) + 2, s->n_chunks0, s->d_err, s->st);
+    launch_level0_chunks(s->n, s->chunks0, (uint32_t)(s->n / s->chunk_rows) + 2, s->n_chunks0, s->d_err,
+                         s->chunk_rows, s->st);
     uint32_t herr = 0;
     CU(cudaMemcpyAsync(&herr, s->d_err, sizeof(uint32_t), cudaMemcpyDeviceToHost, s->st));
     CU(cudaStreamSynchronize(s->st));
@@ -617,7 +624,7 @@ int enqueue_tree(cbgpu_session* s, int set, bool prof, int boot_mode, int s_mode
         const size_t slice_cells = (size_t)s->Fs * built_slots * s->B * 2;
         CU(cudaMemsetAsync(s->built, 0, sizeof(ull) * slice_cells * s->world, st));
         const uint32_t max_chunks =
-            (uint32_t)(s->n / kChunkRows + (l == 0 ? 1 : (1u << (l - 1))) + 1);
+            (uint32_t)(s->n / s->chunk_rows + (l == 0 ? 1 : (1u << (l - 1))) + 1);
         rec(e);
         launch_hist(s->bins_rm, s->F_pad, s->F, s->B, s->qstats, l == 0 ? nullptr : s->list,
                     l == 0 ? s->chunks0 : s->chunks, l == 0 ? s->n_chunks0 : s->n_chunks, max_chunks, s->built,
@@ -661,7 +668,7 @@ int enqueue_tree(cbgpu_session* s, int set, bool prof, int boot_mode, int s_mode
                             more ? s->seg_rows + (size_t)np * kSegMax : nullptr,
                             more ? s->seg_base + (size_t)np * kSegMax : nullptr,
                             more ? s->cursor + (size_t)np * kSegMax : nullptr, s->chunks,
-                            (uint32_t)s->chunk_cap, s->n_chunks, s->ts, st);
+                            (uint32_t)s->chunk_cap, s->n_chunks, s->ts, s->chunk_rows, st);
             rec(e + 4);
             launches += 2;
         } else {
