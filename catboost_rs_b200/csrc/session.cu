@@ -1034,11 +1034,31 @@ int cbgpu_stage_sample(cbgpu_session* s, const double* sample, int64_t sample_le
         return fail(CBGPU_ERR_INVALID, "two staged samples already wait for their grow calls");
     CU(cudaSetDevice(s->device));
     if (!s->copy_st) {
-        CU(cudaStreamCreateWithFlags(&s->copy_st, cudaStreamNonBlocking));
+        // all or nothing: a failed setup leaves no half-built staging state
+        cudaStream_t cs = nullptr;
+        double* buf[2] = {nullptr, nullptr};
+        cudaEvent_t done[2] = {nullptr, nullptr}, fr[2] = {nullptr, nullptr};
+        cudaError_t e = cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking);
+        for (int k = 0; k < 2 && e == cudaSuccess; ++k) {
+            e = cudaMalloc(&buf[k], sizeof(double) * std::max<int64_t>(s->n, 1));
+            if (e == cudaSuccess) e = cudaEventCreateWithFlags(&done[k], cudaEventDisableTiming);
+            if (e == cudaSuccess) e = cudaEventCreateWithFlags(&fr[k], cudaEventDisableTiming);
+        }
+        if (e != cudaSuccess) {
+            for (int k = 0; k < 2; ++k) {
+                if (buf[k]) cudaFree(buf[k]);
+                if (done[k]) cudaEventDestroy(done[k]);
+                if (fr[k]) cudaEventDestroy(fr[k]);
+            }
+            if (cs) cudaStreamDestroy(cs);
+            return fail(e == cudaErrorMemoryAllocation ? CBGPU_ERR_OOM : CBGPU_ERR_CUDA,
+                        "sample staging setup failed: %s", cudaGetErrorString(e));
+        }
+        s->copy_st = cs;
         for (int k = 0; k < 2; ++k) {
-            CU(cudaMalloc(&s->stage_buf[k], sizeof(double) * std::max<int64_t>(s->n, 1)));
-            CU(cudaEventCreateWithFlags(&s->stage_done[k], cudaEventDisableTiming));
-            CU(cudaEventCreateWithFlags(&s->stage_free[k], cudaEventDisableTiming));
+            s->stage_buf[k] = buf[k];
+            s->stage_done[k] = done[k];
+            s->stage_free[k] = fr[k];
         }
     }
     const int k = (s->stage_head + s->stage_count) & 1;
