@@ -1335,6 +1335,10 @@ __device__ __forceinline__ void yeti_sample_smem(int64_t g, int lane, const Rng6
     lcg_jump((uint64_t)g, ag, dg);
     Rng64 first = base;  // draw (permutation p, document lane)
     first.advance((uint64_t)lane);
+    // the decay weights of this lane's adjacent positions d = 1 + lane + 32 sl
+    double dpw[kSlots];
+#pragma unroll
+    for (int sl = 0; sl < kSlots; ++sl) dpw[sl] = 1 + lane + 32 * sl < g ? decay_pow[lane + 32 * sl] : 0.0;
     __syncwarp();
     for (int p = 0; p < perms; ++p) {
         double k[kSlots];
@@ -1366,19 +1370,33 @@ __device__ __forceinline__ void yeti_sample_smem(int64_t g, int lane, const Rng6
         for (int sl = 0; sl < kSlots; ++sl)
             if (lane + 32 * sl < g) ix[pos[sl]] = lane + 32 * sl;
         __syncwarp();
-        for (int64_t d = 1 + lane; d < g; d += 32) {
-            const int32_t fi = ix[d - 1], se = ix[d];
-            const float rf = rel[fi], rs = rel[se];
-            const float pw =
-                __double2float_rn(__dmul_rn(__dmul_rn(0.15, decay_pow[d - 1]), (double)fabsf(__fsub_rn(rf, rs))));
-            if (rf > rs) cwg[fi * g + se] = __fadd_rn(cwg[fi * g + se], pw);
-            else if (rf < rs) cwg[se * g + fi] = __fadd_rn(cwg[se * g + fi], pw);
+        // a permutation's adjacent pairs are distinct, so are their cells:
+        // all of a lane's loads go out before its stores
+        int64_t cell[kSlots];
+        float pwv[kSlots], old[kSlots];
+#pragma unroll
+        for (int sl = 0; sl < kSlots; ++sl) {
+            const int64_t d = 1 + lane + 32 * sl;
+            cell[sl] = -1;
+            pwv[sl] = 0.0f;
+            if (d < g) {
+                const int32_t fi = ix[d - 1], se = ix[d];
+                const float rf = rel[fi], rs = rel[se];
+                pwv[sl] = __double2float_rn(__dmul_rn(__dmul_rn(0.15, dpw[sl]), (double)fabsf(__fsub_rn(rf, rs))));
+                if (rf > rs) cell[sl] = (int64_t)fi * g + se;
+                else if (rf < rs) cell[sl] = (int64_t)se * g + fi;
+            }
         }
+#pragma unroll
+        for (int sl = 0; sl < kSlots; ++sl) old[sl] = cell[sl] >= 0 ? cwg[cell[sl]] : 0.0f;
+#pragma unroll
+        for (int sl = 0; sl < kSlots; ++sl)
+            if (cell[sl] >= 0) cwg[cell[sl]] = __fadd_rn(old[sl], pwv[sl]);
         __syncwarp();
     }
 }
 
-__global__ void __launch_bounds__(kYetiWarps * 32) rk_yeti_sample_kernel(
+__global__ void __launch_bounds__(kYetiWarps * 32, 6) rk_yeti_sample_kernel(
     int n_groups, const int64_t* __restrict__ goff, const double* __restrict__ ap, const double* __restrict__ target,
     int perms, const double* __restrict__ decay_pow, const uint64_t* __restrict__ seeds,
     const int64_t* __restrict__ cwoff, float* __restrict__ cw, int32_t* __restrict__ idx,
@@ -1473,9 +1491,9 @@ constexpr int kYetiMaskWords = kYetiMaskDocs / 32;
 // winners w > x.  The sums are the dense walk's, term for term.
 __device__ __forceinline__ void yeti_der_sparse(int64_t g, const float* __restrict__ cwg,
                                                 const double* __restrict__ exg, float qw, float den,
-                                                uint32_t* __restrict__ rmask, double* __restrict__ d1,
-                                                double* __restrict__ d2, double* __restrict__ eff, int lane,
-                                                bool& finite) {
+                                                uint32_t* __restrict__ rmask, uint32_t* __restrict__ cmask_s,
+                                                double* __restrict__ d1, double* __restrict__ d2,
+                                                double* __restrict__ eff, int lane, bool& finite) {
     const int W = (int)((g + 31) >> 5);
     uint32_t cmask[kYetiMaskWords][kYetiMaskWords];  // [column slot][row word]
 #pragma unroll
@@ -1513,57 +1531,60 @@ __device__ __forceinline__ void yeti_der_sparse(int64_t g, const float* __restri
             }
         }
     }
+    // column masks to shared memory, so the walk below indexes them at run
+    // time instead of unrolling (the unrolled walk overflowed the
+    // instruction cache)
+#pragma unroll
+    for (int k = 0; k < kYetiMaskWords; ++k)
+#pragma unroll
+        for (int w = 0; w < kYetiMaskWords; ++w) cmask_s[(lane + 32 * k) * kYetiMaskWords + w] = cmask[k][w];
     __syncwarp();
-#pragma unroll
-    for (int k = 0; k < kYetiMaskWords; ++k) {
-        if (k >= W) break;
+#pragma unroll 1
+    for (int k = 0; k < W; ++k) {
         const int64_t x = lane + 32 * k;
-        if (x < g) {
-            const double ewx = exg[x];
-            double a1 = 0.0, a2 = 0.0, ae = 0.0, wd = 0.0, wd2 = 0.0, c, cp, q;
-            // winners of column x: below x, then (after the row) above x
-            auto column = [&](bool above) {
-#pragma unroll
-                for (int rw = 0; rw < kYetiMaskWords; ++rw) {
-                    uint32_t m = cmask[k][rw];
-                    const int lo = rw * 32;
-                    // bits w < x (or w > x) of this word
-                    const int64_t cut = x - lo;  // bit index of x in this word
-                    if (!above) m = cut <= 0 ? 0u : (cut >= 32 ? m : m & ((1u << cut) - 1u));
+        if (x >= g) continue;
+        const double ewx = exg[x];
+        double a1 = 0.0, a2 = 0.0, ae = 0.0, wd = 0.0, wd2 = 0.0, c, cp, q;
+        // phases: 0 = winners w < x of column x, 1 = row x's losers, 2 = winners w > x
+#pragma unroll 1
+        for (int ph = 0; ph < 3; ++ph) {
+#pragma unroll 1
+            for (int rw = 0; rw < W; ++rw) {
+                uint32_t m;
+                if (ph == 1) {
+                    m = rmask[x * kYetiMaskWords + rw];
+                } else {
+                    m = cmask_s[x * kYetiMaskWords + rw];
+                    const int64_t cut = x - rw * 32;  // bit index of x in this word
+                    if (ph == 0) m = cut <= 0 ? 0u : (cut >= 32 ? m : m & ((1u << cut) - 1u));
                     else m = cut < 0 ? m : (cut >= 31 ? 0u : m & ~((2u << cut) - 1u));
-                    while (m) {
-                        const int w = lo + __ffs(m) - 1;
-                        m &= m - 1;
-                        if (yeti_cell(cwg[(int64_t)w * g + x], qw, den, ewx, exg[w], c, cp, q)) {
+                }
+                while (m) {
+                    const int o = rw * 32 + __ffs(m) - 1;  // loser (row) or winner (column)
+                    m &= m - 1;
+                    const bool row = ph == 1;
+                    const float cv = row ? cwg[x * g + o] : cwg[(int64_t)o * g + x];
+                    if (yeti_cell(cv, qw, den, row ? exg[o] : ewx, row ? ewx : exg[o], c, cp, q)) {
+                        if (row) {
+                            wd = __dadd_rn(wd, cp);
+                            wd2 = __dadd_rn(wd2, q);
+                        } else {
                             a1 = __dsub_rn(a1, cp);
                             a2 = __dadd_rn(a2, q);
-                            ae = __dadd_rn(ae, c);
                         }
-                    }
-                }
-            };
-            column(false);
-#pragma unroll
-            for (int lw = 0; lw < kYetiMaskWords; ++lw) {
-                uint32_t m = lw < W ? rmask[x * kYetiMaskWords + lw] : 0u;
-                while (m) {
-                    const int l = lw * 32 + __ffs(m) - 1;
-                    m &= m - 1;
-                    if (yeti_cell(cwg[x * g + l], qw, den, exg[l], ewx, c, cp, q)) {
-                        wd = __dadd_rn(wd, cp);
-                        wd2 = __dadd_rn(wd2, q);
                         ae = __dadd_rn(ae, c);
                     }
                 }
             }
-            a1 = __dadd_rn(a1, wd);
-            a2 = __dadd_rn(a2, wd2);
-            column(true);
-            d1[x] = a1;
-            d2[x] = a2;
-            if (eff) eff[x] = ae;
-            finite &= isfinite(a1) && isfinite(a2);
+            if (ph == 1) {  // the winner row ends
+                a1 = __dadd_rn(a1, wd);
+                a2 = __dadd_rn(a2, wd2);
+            }
         }
+        d1[x] = a1;
+        d2[x] = a2;
+        if (eff) eff[x] = ae;
+        finite &= isfinite(a1) && isfinite(a2);
     }
 }
 
@@ -1580,6 +1601,7 @@ __global__ void __launch_bounds__(kYetiWarps * 32) rk_yeti_der_kernel(
     int perms, const int64_t* __restrict__ cwoff, const float* __restrict__ cw, double* __restrict__ d1,
     double* __restrict__ d2, double* __restrict__ eff, double* __restrict__ ex, McState* __restrict__ ms) {
     __shared__ uint32_t s_rmask[kYetiWarps][kYetiMaskDocs * kYetiMaskWords];
+    __shared__ uint32_t s_cmask[kYetiWarps][kYetiMaskDocs * kYetiMaskWords];
     const int lane = threadIdx.x & 31;
     const int gi = blockIdx.x * kYetiWarps + (threadIdx.x >> 5);
     if (gi >= n_groups) return;  // warp-uniform
@@ -1592,8 +1614,8 @@ __global__ void __launch_bounds__(kYetiWarps * 32) rk_yeti_der_kernel(
     __syncwarp();
     bool finite = true;
     if (qw_finite && g <= kYetiMaskDocs) {
-        yeti_der_sparse(g, cwg, ex + b, qw, den, s_rmask[threadIdx.x >> 5], d1 + b, d2 + b, eff ? eff + b : nullptr,
-                        lane, finite);
+        yeti_der_sparse(g, cwg, ex + b, qw, den, s_rmask[threadIdx.x >> 5], s_cmask[threadIdx.x >> 5], d1 + b,
+                        d2 + b, eff ? eff + b : nullptr, lane, finite);
         if (__any_sync(0xffffffffu, !finite) && lane == 0) atomicOr(&ms->err, kMcErrNonFinite);
         return;
     }
