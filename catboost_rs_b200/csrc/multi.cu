@@ -731,6 +731,7 @@ struct RkLossParams {
     const double* lm_den;    // [max group size]
     const double* lm_ideal;  // [n_groups]
     int32_t* lm_order;       // [n] group-local sort scratch
+    int32_t lm_no_op;        // metric MRR / ERR / MAP: zero ders (ranking_der.rs:574-581)
 };
 constexpr double kPairwisePrior = 0.1;  // PairwiseNonDiagReg default (oblivious_tree_options.cpp:16)
 
@@ -768,7 +769,8 @@ __global__ void rk_der_kernel(int n_groups, int mode, const int64_t* __restrict_
             d1[i] = 0.0;
             d2[i] = 0.0;
         }
-        if (cnt > 1) {
+        // MRR / ERR / MAP: the reference's arms leave the ders at zero
+        if (cnt > 1 && !lp.lm_no_op) {
             int32_t* ord = lp.lm_order + b;
             const double* ap = approx + b;
             const double* tg = target + b;
@@ -2108,6 +2110,7 @@ struct cbgpu_multi_session {
     double lm_sigma = 1.0;
     int64_t lm_top = -1;
     int32_t lm_norm = 1;
+    int32_t lm_no_op = 0;  // LambdaMart metric MRR / ERR / MAP
     std::vector<int64_t> h_goff;
     double *d_lmden = nullptr, *d_lmideal = nullptr;
     int32_t* d_lmorder = nullptr;
@@ -2560,8 +2563,9 @@ int cbgpu_rank_begin_raw(const cbgpu_begin_args* a, const int64_t* group_offsets
                                             "num_estimations >= 1");
     }
     if (mode == kRankLambdaMart) {
-        if (params && params->lambdamart_metric != 0 && params->lambdamart_metric != 1)
-            return mfail(CBGPU_DECLINED, "rank_begin: LambdaMart covers the NDCG / DCG metrics");
+        if (params && (params->lambdamart_metric < 0 || params->lambdamart_metric > 4))
+            return mfail(CBGPU_ERR_INVALID, "rank_begin: LambdaMart metric %d is not NDCG / DCG / MRR / ERR / MAP",
+                         params->lambdamart_metric);
         if (!(std::isfinite(lm_sigma) && lm_sigma > 0.0) || !(lm_top == -1 || lm_top > 0))
             return mfail(CBGPU_ERR_INVALID, "rank_begin: LambdaMart needs sigma > 0 and top > 0 or -1");
     }
@@ -2668,6 +2672,7 @@ int cbgpu_rank_begin_raw(const cbgpu_begin_args* a, const int64_t* group_offsets
         s->lm_sigma = lm_sigma;
         s->lm_top = lm_top;
         s->lm_norm = params ? (params->lambdamart_norm ? 1 : 0) : 1;
+        s->lm_no_op = params && params->lambdamart_metric >= 2 ? 1 : 0;
         s->h_goff.assign(group_offsets, group_offsets + n_groups + 1);
         s->yeti_perms = yeti_perms;
         s->yeti_decay = yeti_decay;
@@ -3006,7 +3011,7 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
         rk_der_kernel<<<(unsigned)((s->n_groups + 127) / 128), 128, 0, st>>>(
             s->n_groups, s->rank_mode, s->d_goff, s->d_cstart, s->d_closer, s->approx, s->d_tgt, s->weight,
             RkLossParams{s->sm_lambda, s->sm_beta, s->lm_sigma, s->lm_top, s->lm_norm, s->d_lmden, s->d_lmideal,
-                         s->d_lmorder},
+                         s->d_lmorder, s->lm_no_op},
             s->wd1, s->d_der2, s->d_ms);
     } else {
         mc_der_kernel<<<g, kMcThreads, 0, st>>>(n, K, s->approx, s->target, s->weight, s->leaf, s->leaf_lrv, L,

@@ -387,7 +387,9 @@ typedef struct {
     double lambdamart_sigma;   /* LambdaMart sigma (runtime.rs:374-388, default 1.0) */
     int64_t lambdamart_top;    /* LambdaMart top; -1 = the whole group (default) */
     int32_t lambdamart_norm;   /* LambdaMart norm (default 1) */
-    int32_t lambdamart_metric; /* 0 = NDCG (default), 1 = DCG; MRR / ERR / MAP decline */
+    int32_t lambdamart_metric; /* 0 = NDCG (default), 1 = DCG, 2 = MRR, 3 = ERR, 4 = MAP; the last
+                                  three give zero ders, as the reference's no-op arms
+                                  (ranking_der.rs:574-581) */
     int32_t yeti_permutations; /* YetiRank permutations (default 10) */
     double yeti_decay;         /* YetiRank decay (default 0.85) */
     int32_t srank_metric;      /* StochasticRank metric: 0 = NDCG, 1 = DCG; others decline */

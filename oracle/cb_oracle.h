@@ -259,6 +259,7 @@ typedef struct {
     double srank_sigma;            /* StochasticRank sigma (default 1.0) */
     double srank_mu;               /* StochasticRank mu (default 0.0) */
     int32_t srank_num_estimations; /* StochasticRank num_estimations (default 1) */
+    int32_t lambdamart_no_op;      /* LambdaMart metric MRR / ERR / MAP: zero ders (ranking_der.rs:574-581) */
 } orc_rank_args;
 
 /* YetiRank's sampler for one group (sample_pairs, crates/cb-train/src/

@@ -909,8 +909,11 @@ int orc_train_ranking(const orc_rank_args* a, orc_rank_out* o) {
             const int64_t b = a->group_offsets[g], e = a->group_offsets[g + 1];
             if (e <= b) continue;
             if (a->loss == ORC_RANK_LAMBDAMART) {
-                lambdamart_group(approx + b, a->target + b, e - b, a->lambdamart_sigma, a->lambdamart_top,
-                                 a->lambdamart_norm, lm_order, tmp, d1 + b, d2 + b);
+                /* MRR / ERR / MAP: the reference accepts the metric and leaves
+                 * the group's ders at zero (ranking_der.rs:574-581) */
+                if (!a->lambdamart_no_op)
+                    lambdamart_group(approx + b, a->target + b, e - b, a->lambdamart_sigma, a->lambdamart_top,
+                                     a->lambdamart_norm, lm_order, tmp, d1 + b, d2 + b);
             } else if (a->loss == ORC_RANK_QUERYSOFTMAX) {
                 const double beta = a->softmax_beta, lambda = a->softmax_lambda;
                 double max_a = -DBL_MAX;

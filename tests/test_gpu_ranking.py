@@ -119,6 +119,25 @@ def test_weighted_ranking_matches_oracle(cb, loss, lam, beta):
     assert np.max(np.abs(m.staged - o.staged)) <= TOL
 
 
+@pytest.mark.parametrize("metric", ["MRR", "ERR", "MAP"])
+def test_lambdamart_no_op_metrics_match_oracle(cb, metric):
+    # the reference accepts LambdaMart's MRR / ERR / MAP and leaves every der
+    # at zero (ranking_der.rs:574-581): zero leaves, the first-wins split
+    X, y, offsets, pairs = _ranking_data(40, 5, 32)
+    n, F = X.shape
+    borders = [oracle.select_borders(X[:, f], 16) for f in range(F)]
+    fp = cb.FitParams(loss="LambdaMart", depth=3, iterations=2, learning_rate=0.2, l2_leaf_reg=3.0,
+                      boost_from_average=False, lambdamart_metric=metric)
+    m = cb.fit_ranking([X[:, f].copy() for f in range(F)], borders, y, offsets, fp, staged=True)
+    bins = oracle.quantize(X.T.copy(), borders)
+    o = oracle.train_ranking(bins, [len(b) for b in borders], y, offsets, loss="LambdaMart", depth=3, iterations=2,
+                             learning_rate=0.2, l2_leaf_reg=3.0, lambdamart_metric=metric)
+    np.testing.assert_array_equal(m.split_feature, o.split_feature)
+    np.testing.assert_array_equal(m.split_bin, o.split_bin)
+    assert not np.any(m.raw_leaf_values) and not np.any(o.raw_leaf_values)
+    assert np.max(np.abs(m.staged - o.staged)) == 0.0
+
+
 @pytest.mark.parametrize("top,norm,sigma", [(-1, True, 1.0), (5, True, 2.0), (-1, False, 0.5), (300, True, 1.0)])
 def test_lambdamart_matches_oracle(cb, top, norm, sigma):
     # groups of 20-120 documents: the per-group sort, the top cut and the norm rescale
@@ -349,10 +368,6 @@ def test_ranking_declines_and_errors(cb):
     ok = rt.begin_ranking_raw("PairLogitPairwise", 9, True, 1, "Cosine", cols, borders, None, n, F, nb, 0.3, 3.0,
                               cb.DeviceTrainConfig(), offsets, pairs, l2_leaf_reg=3.0)
     assert not ok and "depth" in rt.decline_reason
-    rt = cb.B200MultiRuntime()  # LambdaMart covers NDCG / DCG only
-    ok = rt.begin_ranking_raw("LambdaMart", 3, True, 1, "Cosine", cols, borders, None, n, F, nb, 0.3, 3.0,
-                              cb.DeviceTrainConfig(), offsets, None, lambdamart_metric="MRR")
-    assert not ok and "NDCG" in rt.decline_reason
     with pytest.raises(CbGpuError, match="sigma"):
         cb.B200MultiRuntime().begin_ranking_raw("LambdaMart", 3, True, 1, "Cosine", cols, borders, None, n, F, nb,
                                                 0.3, 3.0, cb.DeviceTrainConfig(), offsets, None, lambdamart_sigma=0.0)

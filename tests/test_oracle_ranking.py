@@ -148,3 +148,19 @@ def test_stochasticrank_noise_matches_trainer_log():
     bases = oracle.yeti_recalc_seeds(20260617, 5, 4, 2, 5)[:, [0, 2]].ravel()
     valid = {(int(b) + g) % 2**64 for b in bases for g in range(5)}
     assert {int(s) for s in seeds} <= valid
+
+
+def test_lambdamart_no_op_metrics_leave_zero_ders():
+    # MRR / ERR / MAP: the reference accepts the metric and leaves every der at
+    # zero (crates/cb-compute/src/ranking_der.rs:574-581), so the leaves are 0
+    rs = np.random.RandomState(4)
+    offsets = np.array([0, 7, 15, 30, 41], dtype=np.int64)
+    n = int(offsets[-1])
+    bins = rs.randint(0, 9, size=(3, n)).astype(np.uint8)
+    y = rs.randint(0, 4, size=n).astype(np.float64)
+    kw = dict(loss="LambdaMart", depth=2, iterations=2, learning_rate=0.3, l2_leaf_reg=1.0)
+    base = oracle.train_ranking(bins, [8, 8, 8], y, offsets, **kw)
+    assert np.any(base.raw_leaf_values)  # NDCG trains
+    for metric in ("MRR", "ERR", "MAP"):
+        o = oracle.train_ranking(bins, [8, 8, 8], y, offsets, lambdamart_metric=metric, **kw)
+        assert not np.any(o.raw_leaf_values) and not np.any(o.staged)
