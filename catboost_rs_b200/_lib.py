@@ -20,7 +20,7 @@ class RankParams(C.Structure):
                 ("lambdamart_sigma", C.c_double), ("lambdamart_top", C.c_int64), ("lambdamart_norm", C.c_int32),
                 ("lambdamart_metric", C.c_int32), ("yeti_permutations", C.c_int32), ("yeti_decay", C.c_double),
                 ("srank_metric", C.c_int32), ("srank_num_estimations", C.c_int32), ("srank_sigma", C.c_double),
-                ("srank_mu", C.c_double)]
+                ("srank_mu", C.c_double), ("pair_weight", C.c_void_p)]
 
 
 class BeginArgs(C.Structure):

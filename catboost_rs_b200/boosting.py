@@ -279,13 +279,14 @@ def normalize_leaf_values(pairwise: bool, lr: float, leaf_weights, raw) -> np.nd
 
 def fit_ranking(float_columns: Sequence[np.ndarray], borders: Sequence[Sequence[float]], target, group_offsets,
                 params: FitParams, pairs=None, weights=None, *, staged: bool = False,
-                device: int = 0) -> RankingModel:
+                device: int = 0, pair_weights=None) -> RankingModel:
     """QueryRMSE / QuerySoftMax / LambdaMart / YetiRank / StochasticRank /
     PairLogit / PairLogitPairwise fit (params.loss) on raw f32 columns with fixed borders:
     cb-train's grouped
     loop (pointwise histograms with Newton or, for QuerySoftMax, Gradient
     leaves; or pairwise scoring and Cholesky leaves) over the device's ranking
-    arm; leaf normalisation on the host as cb-train does it."""
+    arm; leaf normalisation on the host as cb-train does it.  pair_weights
+    (one per pair, default 1) weight PairLogit's pairs."""
     p = params
     cols = [np.ascontiguousarray(c, dtype=np.float32) for c in float_columns]
     F = len(cols)
@@ -305,7 +306,7 @@ def fit_ranking(float_columns: Sequence[np.ndarray], borders: Sequence[Sequence[
                               lambdamart_norm=p.lambdamart_norm, lambdamart_metric=p.lambdamart_metric,
                               yeti_permutations=p.yeti_permutations, yeti_decay=p.yeti_decay,
                               srank_metric=p.srank_metric, srank_sigma=p.srank_sigma, srank_mu=p.srank_mu,
-                              srank_num_estimations=p.srank_num_estimations)
+                              srank_num_estimations=p.srank_num_estimations, pair_weights=pair_weights)
     if not ok:
         raise RuntimeError(f"device declined: {rt.decline_reason}")
     T, D = p.iterations, p.depth

@@ -893,7 +893,7 @@ constexpr int kYetiWarps = 4;  // groups per 128-thread block (warp-per-group ra
 // (the PairLogit arm of rk_der_kernel, ranking_der.rs:400-440, restated per
 // document).  The sequential loop visits winners in ascending order and each
 // winner's competitors in input order: a document's der1 / der2 receive, in
-// that order, -p (and p (p - 1)) for each pair it loses to a winner at or
+// that order, -w p (and w p (p - 1)) for each pair of weight w it loses to a winner at or
 // below its own index -- its own self pairs included, as they come while its
 // competitor list runs -- then its own list's sums, then the pairs it loses to
 // later winners.  Its loser slots (lstart / lpair, ascending slot index) are
@@ -901,8 +901,8 @@ constexpr int kYetiWarps = 4;  // groups per 128-thread block (warp-per-group ra
 __global__ void __launch_bounds__(kYetiWarps * 32) rk_pairlogit_der_kernel(
     int n_groups, const int64_t* __restrict__ goff, const int64_t* __restrict__ cstart,
     const int64_t* __restrict__ closer, const int64_t* __restrict__ pwin, const int64_t* __restrict__ lstart,
-    const int64_t* __restrict__ lpair, const double* __restrict__ approx, double* __restrict__ ex,
-    double* __restrict__ d1, double* __restrict__ d2, McState* __restrict__ ms) {
+    const int64_t* __restrict__ lpair, const double* __restrict__ pairw, const double* __restrict__ approx,
+    double* __restrict__ ex, double* __restrict__ d1, double* __restrict__ d2, McState* __restrict__ ms) {
     const int lane = threadIdx.x & 31;
     const int gi = blockIdx.x * kYetiWarps + (threadIdx.x >> 5);
     if (gi >= n_groups) return;  // warp-uniform
@@ -913,11 +913,12 @@ __global__ void __launch_bounds__(kYetiWarps * 32) rk_pairlogit_der_kernel(
     for (int64_t x = b + lane; x < e; x += 32) {
         const double exx = ex[x];
         double a1 = 0.0, a2 = 0.0;
-        auto lose = [&](int64_t k) {  // x loses pair k: p = e^x / (e^x + e^winner)
+        auto lose = [&](int64_t k) {  // x loses pair k: p = e^x / (e^x + e^winner), weight w
             const double den = __dadd_rn(exx, ex[pwin[k]]);
             const double p = den > 0.0 ? __ddiv_rn(exx, den) : 0.5;
-            a1 = __dsub_rn(a1, __dmul_rn(1.0, p));
-            a2 = __dadd_rn(a2, __dmul_rn(__dmul_rn(1.0, p), __dsub_rn(p, 1.0)));
+            const double wp = __dmul_rn(pairw[k], p);
+            a1 = __dsub_rn(a1, wp);
+            a2 = __dadd_rn(a2, __dmul_rn(wp, __dsub_rn(p, 1.0)));
         };
         int64_t j = lstart[x];
         const int64_t je = lstart[x + 1];
@@ -927,8 +928,9 @@ __global__ void __launch_bounds__(kYetiWarps * 32) rk_pairlogit_der_kernel(
             const double el = ex[closer[k]];
             const double den = __dadd_rn(el, exx);
             const double p = den > 0.0 ? __ddiv_rn(el, den) : 0.5;
-            wd = __dadd_rn(wd, __dmul_rn(1.0, p));
-            wd2 = __dadd_rn(wd2, __dmul_rn(__dmul_rn(1.0, p), __dsub_rn(p, 1.0)));
+            const double wp = __dmul_rn(pairw[k], p);
+            wd = __dadd_rn(wd, wp);
+            wd2 = __dadd_rn(wd2, __dmul_rn(wp, __dsub_rn(p, 1.0)));
         }
         a1 = __dadd_rn(a1, wd);
         a2 = __dadd_rn(a2, wd2);
@@ -2100,6 +2102,7 @@ struct cbgpu_multi_session {
     // closer[k] == doc, ascending), their offsets, exp(approx) scratch
     int64_t *d_lstart = nullptr, *d_lpair = nullptr;
     double* d_pex = nullptr;
+    double* d_pairw = nullptr;  // [n_pairs] pair weight per competitor slot (closer order)
     long long *d_pstat = nullptr, *d_pwsum = nullptr;
     int pw_shift = 0;  // pair weights in the statistics: llrint(w * 2^pw_shift)
     double* d_pwscratch = nullptr;
@@ -2161,6 +2164,7 @@ struct cbgpu_multi_session {
         cudaFree(d_lstart);
         cudaFree(d_lpair);
         cudaFree(d_pex);
+        cudaFree(d_pairw);
         cudaFree(d_pstat);
         cudaFree(d_pwsum);
         cudaFree(d_pwscratch);
@@ -2627,6 +2631,16 @@ int cbgpu_rank_begin_raw(const cbgpu_begin_args* a, const int64_t* group_offsets
     std::vector<int64_t> cstart((size_t)n + 1, 0), closer((size_t)std::max<int64_t>(n_pairs, 1));
     std::vector<double> eff((size_t)n, 0.0);
     std::vector<int64_t> win, lstart, lpair;
+    std::vector<double> slot_w;
+    const double* pair_weight = params ? params->pair_weight : nullptr;
+    if (pair_weight && (mode == kRankPairLogit || mode == kRankPairLogitPairwise)) {
+        for (int64_t k = 0; k < n_pairs; ++k) {
+            if (!std::isfinite(pair_weight[k]))
+                return mfail(CBGPU_ERR_INVALID, "rank_begin: pair %lld has a non-finite weight", (long long)k);
+            if (mode == kRankPairLogitPairwise && pair_weight[k] != 1.0)
+                return mfail(CBGPU_DECLINED, "rank_begin: PairLogitPairwise covers unit pair weights");
+        }
+    }
     if (mode == kRankPairLogit || mode == kRankPairLogitPairwise) {
         for (int64_t k = 0; k < n_pairs; ++k) {
             const int64_t wv = pair_winner[k], lv = pair_loser[k];
@@ -2637,15 +2651,21 @@ int cbgpu_rank_begin_raw(const cbgpu_begin_args* a, const int64_t* group_offsets
         }
         for (int64_t i = 0; i < n; ++i) cstart[(size_t)i + 1] += cstart[(size_t)i];
         std::vector<int64_t> fill(cstart.begin(), cstart.end() - 1);
-        for (int64_t k = 0; k < n_pairs; ++k) closer[(size_t)fill[(size_t)pair_winner[k]]++] = pair_loser[k];
+        slot_w.assign(closer.size(), 1.0);
+        for (int64_t k = 0; k < n_pairs; ++k) {
+            const int64_t at = fill[(size_t)pair_winner[k]]++;
+            closer[(size_t)at] = pair_loser[k];
+            if (pair_weight) slot_w[(size_t)at] = pair_weight[k];
+        }
         win.assign(closer.size(), 0);
         for (int64_t i = 0; i < n; ++i)
             for (int64_t k = cstart[(size_t)i]; k < cstart[(size_t)i + 1]; ++k) win[(size_t)k] = i;
+        // calc_pairwise_weights: each pair adds its weight to both documents
         for (int g = 0; g < n_groups; ++g)
             for (int64_t wi = group_offsets[g]; wi < group_offsets[g + 1]; ++wi)
                 for (int64_t k = cstart[(size_t)wi]; k < cstart[(size_t)wi + 1]; ++k) {
-                    eff[(size_t)wi] += 1.0;
-                    eff[(size_t)closer[(size_t)k]] += 1.0;
+                    eff[(size_t)wi] += slot_w[(size_t)k];
+                    eff[(size_t)closer[(size_t)k]] += slot_w[(size_t)k];
                 }
         if (mode == kRankPairLogit) {
             // loser slots by document, ascending k: by winner, then input order
@@ -2695,6 +2715,7 @@ int cbgpu_rank_begin_raw(const cbgpu_begin_args* a, const int64_t* group_offsets
             if (!rc) rc = mdalloc(&s->d_lstart, lstart.size());
             if (!rc) rc = mdalloc(&s->d_lpair, lpair.size());
             if (!rc) rc = mdalloc(&s->d_pex, (size_t)std::max<int64_t>(n, 1));
+            if (!rc) rc = mdalloc(&s->d_pairw, slot_w.size());
         }
         if (!rc && (mode == kRankYetiRank || mode == kRankYetiRankPairwise)) {
             // group weight: the mean member weight (query_info.rs:180-187)
@@ -2792,6 +2813,8 @@ int cbgpu_rank_begin_raw(const cbgpu_begin_args* a, const int64_t* group_offsets
             e = cudaMemcpy(s->d_lstart, lstart.data(), sizeof(int64_t) * lstart.size(), cudaMemcpyHostToDevice);
         if (e == cudaSuccess && s->d_lpair)
             e = cudaMemcpy(s->d_lpair, lpair.data(), sizeof(int64_t) * lpair.size(), cudaMemcpyHostToDevice);
+        if (e == cudaSuccess && s->d_pairw)
+            e = cudaMemcpy(s->d_pairw, slot_w.data(), sizeof(double) * slot_w.size(), cudaMemcpyHostToDevice);
         if (e != cudaSuccess) rc = mfail(CBGPU_ERR_CUDA, "rank_begin: upload failed: %s", cudaGetErrorString(e));
     }
     if (rc) {
@@ -3005,8 +3028,8 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
                                            s->d_srank_ws, s->d_lmorder, s->wd1, s->d_der2, s->d_ms);
     } else if (s->rank_mode == kRankPairLogit) {
         rk_pairlogit_der_kernel<<<yw, kYetiWarps * 32, 0, st>>>(s->n_groups, s->d_goff, s->d_cstart, s->d_closer,
-                                                                s->d_pwin, s->d_lstart, s->d_lpair, s->approx,
-                                                                s->d_pex, s->wd1, s->d_der2, s->d_ms);
+                                                                s->d_pwin, s->d_lstart, s->d_lpair, s->d_pairw,
+                                                                s->approx, s->d_pex, s->wd1, s->d_der2, s->d_ms);
     } else if (s->rank_mode >= 0) {
         rk_der_kernel<<<(unsigned)((s->n_groups + 127) / 128), 128, 0, st>>>(
             s->n_groups, s->rank_mode, s->d_goff, s->d_cstart, s->d_closer, s->approx, s->d_tgt, s->weight,

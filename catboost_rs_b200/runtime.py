@@ -362,12 +362,13 @@ class B200MultiRuntime(B200Runtime):
                           softmax_lambda=0.01, softmax_beta=1.0, lambdamart_sigma=1.0, lambdamart_top=-1,
                           lambdamart_norm=True, lambdamart_metric="NDCG", yeti_permutations=10,
                           yeti_decay=0.85, srank_metric="DCG", srank_sigma=1.0, srank_mu=0.0,
-                          srank_num_estimations=1) -> bool:
+                          srank_num_estimations=1, pair_weights=None) -> bool:
         """The grouped families (FamilyTreeArgs::Ranking / ::Pairwise) for
         QueryRMSE / QuerySoftMax / LambdaMart / YetiRank / StochasticRank / PairLogit /
         PairLogitPairwise: group offsets
         [n_groups + 1] and, for the pair losses, (winner, loser) global object
-        ids; l2_leaf_reg is the unscaled l2 the pairwise scorer and leaves use
+        ids with optional per-pair weights (Competitor::weight; default 1);
+        l2_leaf_reg is the unscaled l2 the pairwise scorer and leaves use
         (default scaled_l2); QuerySoftMax's lambda and beta; LambdaMart's
         sigma, top, norm and metric (NDCG / DCG); YetiRank's permutations and
         decay (its pairs are sampled on the device); StochasticRank's metric
@@ -386,14 +387,17 @@ class B200MultiRuntime(B200Runtime):
         pr = np.zeros((0, 2), dtype=np.int64) if pairs is None else np.asarray(pairs, dtype=np.int64).reshape(-1, 2)
         pw = np.ascontiguousarray(pr[:, 0])
         pl = np.ascontiguousarray(pr[:, 1])
+        pwt = None if pair_weights is None else np.ascontiguousarray(pair_weights, dtype=np.float64)
+        if pwt is not None and pwt.size != pw.size:
+            raise _lib.CbGpuError(_lib.ERR_INVALID, "LengthMismatch: pair_weights must have one weight per pair")
         a = self._args(loss, depth, boosting_type_is_plain, fold_count, score_function, weight, n,
                        n_features, n_bins, learning_rate, scaled_l2, config)
-        self._keep += [go, pw, pl]
+        self._keep += [go, pw, pl] + ([pwt] if pwt is not None else [])
         rp = _lib.RankParams(-1.0 if l2_leaf_reg is None else float(l2_leaf_reg), float(softmax_lambda),
                              float(softmax_beta), float(lambdamart_sigma), int(lambdamart_top),
                              1 if lambdamart_norm else 0, LAMBDAMART_METRIC[lambdamart_metric],
                              int(yeti_permutations), float(yeti_decay), LAMBDAMART_METRIC[srank_metric],
-                             int(srank_num_estimations), float(srank_sigma), float(srank_mu))
+                             int(srank_num_estimations), float(srank_sigma), float(srank_mu), _ptr(pwt))
         rc = self._L.cbgpu_rank_begin_raw(C.byref(a), _ptr(go), go.size - 1, _ptr(pw), _ptr(pl), pw.size,
                                           C.byref(rp), colptrs, _ptr(flat), _ptr(counts), C.byref(self._s))
         ok = self._finish_begin(rc, n, depth)

@@ -396,6 +396,9 @@ typedef struct {
     int32_t srank_num_estimations; /* StochasticRank num_estimations (default 1) */
     double srank_sigma;        /* StochasticRank sigma (default 1.0) */
     double srank_mu;           /* StochasticRank mu (default 0.0) */
+    const double* pair_weight; /* [n_pairs] per-pair weight (Competitor::weight, query_info.rs:205-250)
+                                  for PairLogit; NULL = 1.0 each.  PairLogitPairwise declines
+                                  weights other than 1 */
 } cbgpu_rank_params;
 
 /* The seam's grouped families (FamilyTreeArgs::Ranking / ::Pairwise,
@@ -422,7 +425,8 @@ typedef struct {
  * the raw l2_leaf_reg and the PairwiseNonDiagReg prior 0.1; depth 1..8.
  *  group_offsets [n_groups + 1] contiguous groups over object order, 0..n;
  *  pair_winner / pair_loser [n_pairs] global object ids of the pairs
- *                (weight 1, both in one group), ignored for QueryRMSE;
+ *                (both in one group; weights in params->pair_weight, else 1),
+ *                ignored for QueryRMSE;
  *  params        cbgpu_rank_params or NULL (defaults).
  * The session is grown with cbgpu_multi_grow_tree at approx_dim 1 (target =
  * the relevance per object); its leaf_values are the raw deltas, and the

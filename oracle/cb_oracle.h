@@ -260,6 +260,7 @@ typedef struct {
     double srank_mu;               /* StochasticRank mu (default 0.0) */
     int32_t srank_num_estimations; /* StochasticRank num_estimations (default 1) */
     int32_t lambdamart_no_op;      /* LambdaMart metric MRR / ERR / MAP: zero ders (ranking_der.rs:574-581) */
+    const double* pair_weight;     /* [n_pairs] Competitor::weight per pair (PairLogit); NULL = 1 */
 } orc_rank_args;
 
 /* YetiRank's sampler for one group (sample_pairs, crates/cb-train/src/

@@ -57,17 +57,19 @@ static double pair_prob(double winner, double loser) {
 }
 
 typedef struct {
-    int64_t* start; /* [n + 1] CSR over winners (global object ids) */
-    int64_t* loser; /* [n_pairs] in pair order per winner */
+    int64_t* start;  /* [n + 1] CSR over winners (global object ids) */
+    int64_t* loser;  /* [n_pairs] in pair order per winner */
+    double* weight;  /* [n_pairs] the pair's Competitor::weight, same order */
 } competitors;
 
 /* build_query_info step 3 (query_info.rs:205-250): pairs in input order,
- * pushed to their winner's row, weight 1.0. */
+ * pushed to their winner's row with their weight (1.0 when none is given). */
 static int build_competitors(const orc_rank_args* a, competitors* c) {
     const int64_t n = a->n;
     c->start = (int64_t*)calloc((size_t)n + 1, sizeof(int64_t));
     c->loser = (int64_t*)malloc(sizeof(int64_t) * (size_t)(a->n_pairs > 0 ? a->n_pairs : 1));
-    if (!c->start || !c->loser) return -1;
+    c->weight = (double*)malloc(sizeof(double) * (size_t)(a->n_pairs > 0 ? a->n_pairs : 1));
+    if (!c->start || !c->loser || !c->weight) return -1;
     for (int64_t k = 0; k < a->n_pairs; ++k) {
         if (a->pair_winner[k] < 0 || a->pair_winner[k] >= n || a->pair_loser[k] < 0 || a->pair_loser[k] >= n)
             return -1;
@@ -77,7 +79,11 @@ static int build_competitors(const orc_rank_args* a, competitors* c) {
     int64_t* fill = (int64_t*)malloc(sizeof(int64_t) * (size_t)(n > 0 ? n : 1));
     if (!fill) return -1;
     for (int64_t i = 0; i < n; ++i) fill[i] = c->start[i];
-    for (int64_t k = 0; k < a->n_pairs; ++k) c->loser[fill[a->pair_winner[k]]++] = a->pair_loser[k];
+    for (int64_t k = 0; k < a->n_pairs; ++k) {
+        const int64_t at = fill[a->pair_winner[k]]++;
+        c->loser[at] = a->pair_loser[k];
+        c->weight[at] = a->pair_weight ? a->pair_weight[k] : 1.0;
+    }
     free(fill);
     return 0;
 }
@@ -845,12 +851,23 @@ int orc_train_ranking(const orc_rank_args* a, orc_rank_out* o) {
         if (a->border_counts[f] + 1 > NB) NB = a->border_counts[f] + 1;
     if (a->loss == ORC_RANK_YETIRANK || a->loss == ORC_RANK_YETIRANK_PAIRWISE) return train_yetirank(a, o, NB);
     if (a->loss == ORC_RANK_STOCHASTICRANK) return train_stochasticrank(a, o, NB);
-    competitors cp = {NULL, NULL};
+    competitors cp = {NULL, NULL, NULL};
     const int pairlogit = a->loss == ORC_RANK_PAIRLOGIT || a->loss == ORC_RANK_PAIRLOGIT_PAIRWISE;
     if (pairlogit && build_competitors(a, &cp) != 0) {
         free(cp.start);
         free(cp.loser);
+        free(cp.weight);
         return -2;
+    }
+    if (a->loss == ORC_RANK_PAIRLOGIT_PAIRWISE && a->pair_weight) {
+        /* the pairwise statistics here take unit pair weights */
+        for (int64_t k = 0; k < a->n_pairs; ++k)
+            if (a->pair_weight[k] != 1.0) {
+                free(cp.start);
+                free(cp.loser);
+                free(cp.weight);
+                return -3;
+            }
     }
     double* w = (double*)calloc((size_t)(n > 0 ? n : 1), sizeof(double));
     for (int64_t i = 0; i < n; ++i) w[i] = a->weights ? a->weights[i] : 1.0;
@@ -875,8 +892,8 @@ int orc_train_ranking(const orc_rank_args* a, orc_rank_out* o) {
         for (int32_t g = 0; g < a->n_groups; ++g)
             for (int64_t wi = a->group_offsets[g]; wi < a->group_offsets[g + 1]; ++wi)
                 for (int64_t k = cp.start[wi]; k < cp.start[wi + 1]; ++k) {
-                    eff[wi] += 1.0;
-                    eff[cp.loser[k]] += 1.0;
+                    eff[wi] += cp.weight[k];
+                    eff[cp.loser[k]] += cp.weight[k];
                 }
     } else {
         for (int64_t i = 0; i < n; ++i) eff[i] = w[i];
@@ -950,7 +967,7 @@ int orc_train_ranking(const orc_rank_args* a, orc_rank_out* o) {
                     for (int64_t k = cp.start[wi]; k < cp.start[wi + 1]; ++k) {
                         const int64_t li = cp.loser[k];
                         const double p = pair_prob(approx[wi], approx[li]);
-                        const double pw = 1.0;
+                        const double pw = cp.weight[k];
                         wd += pw * p;
                         wd2 += pw * p * (p - 1.0);
                         d1[li] -= pw * p;
@@ -1032,6 +1049,7 @@ int orc_train_ranking(const orc_rank_args* a, orc_rank_out* o) {
     }
     free(cp.start);
     free(cp.loser);
+    free(cp.weight);
     free(pairs_w);
     free(pairs_l);
     free(w); free(approx); free(d1); free(d2); free(eff); free(sh); free(tmp); free(leaf); free(lv); free(lw);

@@ -87,7 +87,7 @@ class _RankArgs(C.Structure):
         ("lambdamart_sigma", C.c_double), ("lambdamart_top", C.c_int64), ("lambdamart_norm", C.c_int32),
         ("yeti_permutations", C.c_int32), ("yeti_decay", C.c_double), ("srank_ndcg", C.c_int32),
         ("srank_sigma", C.c_double), ("srank_mu", C.c_double), ("srank_num_estimations", C.c_int32),
-        ("lambdamart_no_op", C.c_int32),
+        ("lambdamart_no_op", C.c_int32), ("pair_weight", C.c_void_p),
     ]
 
 
@@ -471,7 +471,7 @@ def train_ranking(bins_fm, border_counts, target, group_offsets, *, loss="QueryR
                   weights=None, staged=True, softmax_lambda=0.01, softmax_beta=1.0, lambdamart_sigma=1.0,
                   lambdamart_top=-1, lambdamart_norm=True, yeti_permutations=10,
                   yeti_decay=0.85, srank_metric="DCG", srank_sigma=1.0, srank_mu=0.0,
-                  srank_num_estimations=1, lambdamart_metric="NDCG") -> OracleRankFit:
+                  srank_num_estimations=1, lambdamart_metric="NDCG", pair_weights=None) -> OracleRankFit:
     """The reference's grouped-loss CPU loop: QueryRMSE / PairLogit (pointwise histograms, Newton
     leaves), QuerySoftMax (pointwise histograms, Gradient leaves), LambdaMart (NDCG lambdas, Newton
     leaves), YetiRank (sampled pairs, Newton leaves, two approximants), StochasticRank (Monte-Carlo
@@ -485,6 +485,9 @@ def train_ranking(bins_fm, border_counts, target, group_offsets, *, loss="QueryR
     pr = np.zeros((0, 2), dtype=np.int64) if pairs is None else np.ascontiguousarray(pairs, dtype=np.int64)
     pw = np.ascontiguousarray(pr[:, 0])
     pl = np.ascontiguousarray(pr[:, 1])
+    pwt = None if pair_weights is None else np.ascontiguousarray(pair_weights, dtype=np.float64)
+    if pwt is not None and pwt.size != pw.size:
+        raise ValueError("pair_weights must have one weight per pair")
     w = None if weights is None else np.ascontiguousarray(weights, dtype=np.float64)
     L = 1 << depth
     sf = np.empty((iterations, depth), dtype=np.int32)
@@ -496,7 +499,7 @@ def train_ranking(bins_fm, border_counts, target, group_offsets, *, loss="QueryR
                      _p(pl), depth, iterations, learning_rate, l2_leaf_reg, SCORE[score_function], random_seed,
                      softmax_lambda, softmax_beta, lambdamart_sigma, lambdamart_top, int(bool(lambdamart_norm)),
                      yeti_permutations, yeti_decay, 1 if srank_metric == "NDCG" else 0, srank_sigma, srank_mu,
-                     srank_num_estimations, 1 if lambdamart_metric in ("MRR", "ERR", "MAP") else 0)
+                     srank_num_estimations, 1 if lambdamart_metric in ("MRR", "ERR", "MAP") else 0, _p(pwt))
     out = _RankOut(_p(sf), _p(sb), _p(lv), _p(raw), _p(st))
     rc = lib().orc_train_ranking(C.byref(args), C.byref(out))
     if rc != 0:

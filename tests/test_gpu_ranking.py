@@ -119,6 +119,55 @@ def test_weighted_ranking_matches_oracle(cb, loss, lam, beta):
     assert np.max(np.abs(m.staged - o.staged)) <= TOL
 
 
+@pytest.mark.parametrize("depth,score", [(5, "Cosine"), (4, "L2")])
+def test_weighted_pairs_match_oracle(cb, depth, score):
+    # PairLogit with per-pair weights (Competitor::weight): the ders scale by
+    # the weight and the pairwise histogram weights sum it
+    X, y, offsets, pairs = _ranking_data(200, 8, 13 + depth)
+    F = X.shape[1]
+    pwt = np.random.RandomState(depth).choice([0.25, 0.5, 1.0, 2.0, 3.75], size=len(pairs))
+    borders = [oracle.select_borders(X[:, f], 48) for f in range(F)]
+    fp = cb.FitParams(loss="PairLogit", depth=depth, iterations=4, learning_rate=0.3, l2_leaf_reg=3.0,
+                      score_function=score, boost_from_average=False)
+    m = cb.fit_ranking([X[:, f].copy() for f in range(F)], borders, y, offsets, fp, pairs=pairs, staged=True,
+                       pair_weights=pwt)
+    bins = oracle.quantize(X.T.copy(), borders)
+    o = oracle.train_ranking(bins, [len(b) for b in borders], y, offsets, loss="PairLogit", pairs=pairs, depth=depth,
+                             iterations=4, learning_rate=0.3, l2_leaf_reg=3.0, score_function=score,
+                             pair_weights=pwt)
+    np.testing.assert_array_equal(m.split_feature, o.split_feature)
+    np.testing.assert_array_equal(m.split_bin, o.split_bin)
+    assert np.max(np.abs(m.raw_leaf_values - o.raw_leaf_values)) <= TOL
+    assert np.max(np.abs(m.staged - o.staged)) <= TOL
+    # unit weights given explicitly are the unweighted fit
+    u = cb.fit_ranking([X[:, f].copy() for f in range(F)], borders, y, offsets, fp, pairs=pairs, staged=True,
+                       pair_weights=np.ones(len(pairs)))
+    v = cb.fit_ranking([X[:, f].copy() for f in range(F)], borders, y, offsets, fp, pairs=pairs, staged=True)
+    np.testing.assert_array_equal(u.staged, v.staged)
+
+
+def test_weighted_pairs_rules(cb):
+    from catboost_rs_b200 import CbGpuError
+    X, y, offsets, pairs = _ranking_data(20, 4, 3)
+    n, F = X.shape
+    borders = [oracle.select_borders(X[:, f], 16) for f in range(F)]
+    cols = [X[:, f].copy() for f in range(F)]
+    nb = max(len(b) for b in borders) + 1
+    w = np.full(len(pairs), 2.0)
+    rt = cb.B200MultiRuntime()  # the pairwise scorer takes unit pair weights
+    ok = rt.begin_ranking_raw("PairLogitPairwise", 3, True, 1, "Cosine", cols, borders, None, n, F, nb, 0.3, 3.0,
+                              cb.DeviceTrainConfig(), offsets, pairs, pair_weights=w)
+    assert not ok and "unit pair weights" in rt.decline_reason
+    w[3] = np.nan
+    with pytest.raises(CbGpuError, match="non-finite weight"):
+        cb.B200MultiRuntime().begin_ranking_raw("PairLogit", 3, True, 1, "Cosine", cols, borders, None, n, F, nb,
+                                                0.3, 3.0, cb.DeviceTrainConfig(), offsets, pairs, pair_weights=w)
+    with pytest.raises(CbGpuError, match="one weight per pair"):
+        cb.B200MultiRuntime().begin_ranking_raw("PairLogit", 3, True, 1, "Cosine", cols, borders, None, n, F, nb,
+                                                0.3, 3.0, cb.DeviceTrainConfig(), offsets, pairs,
+                                                pair_weights=np.ones(2))
+
+
 @pytest.mark.parametrize("metric", ["MRR", "ERR", "MAP"])
 def test_lambdamart_no_op_metrics_match_oracle(cb, metric):
     # the reference accepts LambdaMart's MRR / ERR / MAP and leaves every der

@@ -164,3 +164,22 @@ def test_lambdamart_no_op_metrics_leave_zero_ders():
     for metric in ("MRR", "ERR", "MAP"):
         o = oracle.train_ranking(bins, [8, 8, 8], y, offsets, lambdamart_metric=metric, **kw)
         assert not np.any(o.raw_leaf_values) and not np.any(o.staged)
+
+
+def test_pairlogit_pair_weight_scales_ders():
+    # the reference's vector (crates/cb-compute/src/ranking_der_test.rs:314):
+    # approx [0, 0], document 0 beats document 1 with weight w: der1 = [w/2,
+    # -w/2], der2 = [-w/4, -w/4].  A depth-1 tree splits the two documents
+    # apart, so each raw Newton leaf is der1 / (-der2 + c) for the same l2
+    # term c: w/2 / (w/4 + c) for the winner's leaf.
+    bins = np.array([[1, 0]], dtype=np.uint8)
+    y = np.array([1.0, 0.0])
+    offsets = np.array([0, 2], dtype=np.int64)
+    pairs = np.array([[0, 1]], dtype=np.int64)
+    kw = dict(loss="PairLogit", pairs=pairs, depth=1, iterations=1, learning_rate=0.1, l2_leaf_reg=1.0)
+    r1 = oracle.train_ranking(bins, [1], y, offsets, **kw).raw_leaf_values[0]
+    r2 = oracle.train_ranking(bins, [1], y, offsets, pair_weights=[2.0], **kw).raw_leaf_values[0]
+    c = 0.5 / r1[1] - 0.25  # from the unit-weight fit
+    assert c > 0
+    assert np.isclose(r1[0], -r1[1]) and np.isclose(r2[0], -r2[1])
+    assert np.isclose(r2[1], 1.0 / (0.5 + c), rtol=1e-12)
