@@ -320,7 +320,8 @@ def main():
     ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4, 5],
                     help="BASELINE config: 2 (default) or 5 (RMSE 50M x 500, depth 10, MVS) on this file's "
                          "scalar session; 3 (MultiClass) or 4 (ranking) from bench_configs.py")
-    ap.add_argument("--variant", default=None, help="config 3: onehot | bernoulli; config 4: yetirank | pairlogit")
+    ap.add_argument("--variant", default=None, help="config 3: onehot | bernoulli; config 4: yetirank | pairlogit | "
+                                                         "yetirankpairwise | pairlogitpairwise")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.config == 5:  # its shape unless overridden on the command line

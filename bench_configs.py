@@ -17,8 +17,9 @@ the config's shapes and distributions (no public dataset is named).
   20-120, 136 features (half log-normal counts, half U(0,1) ratios),
   border_count 128, relevance 0-4 from a noisy linear score per query,
   depth 6; YetiRank (pairs sampled on the device) or PairLogit (pairs of
-  differently relevant documents, at most 200 per query)
-  (`--variant yetirank|pairlogit`).
+  differently relevant documents, at most 200 per query), each also with
+  the pairwise scorer and Cholesky pairwise leaves
+  (`--variant yetirank|pairlogit|yetirankpairwise|pairlogitpairwise`).
 - config 5: RMSE, 50M rows x 500 N(0,1) features, border_count 128, sparse
   linear target + noise, depth 10, MVS subsample 0.8, on the scalar session
   (the same path as config 2); document-sharded under torchrun.
@@ -158,14 +159,16 @@ def run_config4(args):
     F, n = X.shape
     borders = _borders(X, 128, args.seed)
     cols = [np.ascontiguousarray(X[f]) for f in range(F)]
-    loss = {"yetirank": "YetiRank", "pairlogit": "PairLogit"}[variant]
-    pairs = config4_pairs(rel, offsets, args.seed) if variant == "pairlogit" else None
+    loss = {"yetirank": "YetiRank", "pairlogit": "PairLogit", "pairlogitpairwise": "PairLogitPairwise",
+            "yetirankpairwise": "YetiRankPairwise"}[variant]
+    pairs = config4_pairs(rel, offsets, args.seed) if variant.startswith("pairlogit") else None
     rt = cb.B200MultiRuntime()
     cfg = cb.DeviceTrainConfig(bootstrap_type="No", rng_seed=0, bias=0.0)
     nb = max(len(b) for b in borders) + 1
     lr = float(np.float32(0.1))
     assert rt.begin_ranking_raw(loss, 6, True, 1, "Cosine", cols, borders, None, n, F, nb, lr, 3.0, cfg,
-                                offsets, pairs=pairs), rt.decline_reason
+                                offsets, pairs=pairs, l2_leaf_reg=3.0 if loss.endswith("Pairwise") else None), \
+        rt.decline_reason
     try:
         for _ in range(args.warmup):
             rt.grow_tree_on_device(None, rel, [], leaf_of_bytes=0, resident_approx=True)
