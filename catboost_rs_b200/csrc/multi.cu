@@ -1736,6 +1736,51 @@ __global__ void rk_pairstat_kernel(int64_t n_pairs, int64_t n, int P, int NB, co
     }
 }
 
+// The same statistics at levels of at most kPsSmemLeaves parents, where one
+// feature's whole table (P^2 NB (smaller, greater) cells) fits in shared
+// memory: a block takes one feature and a share of the pairs, adds exactly
+// into (lo, hi) 32-bit word pairs (add_split64), and flushes its table with
+// one global atomic per non-zero cell -- instead of two contended global
+// atomics per (pair, feature).  Integer sums: the same result in any order.
+constexpr int kPsSmemLeaves = 8;
+constexpr int kPsThreads = 1024;
+__global__ void __launch_bounds__(kPsThreads) rk_pairstat_smem_kernel(
+    int64_t n_pairs, int64_t n, int P, int NB, const int64_t* __restrict__ pw, const int64_t* __restrict__ pl,
+    const uint8_t* __restrict__ bins_fm, const uint16_t* __restrict__ leaf, int pw_shift,
+    long long* __restrict__ stats) {
+    extern __shared__ uint32_t pst[];  // lo words [cells], then hi words [cells]
+    const int f = blockIdx.y;
+    const uint8_t* col = bins_fm + (size_t)f * (size_t)n;
+    const int cells = P * P * NB * 2;
+    uint32_t* lo = pst;
+    uint32_t* hi = pst + cells;
+    for (int k = threadIdx.x; k < 2 * cells; k += blockDim.x) pst[k] = 0u;
+    __syncthreads();
+    const long long q = -(1ll << pw_shift);
+    for (int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < n_pairs; k += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t w = pw[k], l = pl[k];
+        if (w == l) continue;
+        const int wb = col[w], lb = col[l], wl = leaf[w], ll = leaf[l];
+        if (wl >= P || ll >= P || wb >= NB || lb >= NB) continue;
+        int c0, c1;  // pw_stat_pair's two cells
+        if (wb > lb) {
+            c0 = ((ll * P + wl) * NB + lb) * 2;
+            c1 = ((ll * P + wl) * NB + wb) * 2 + 1;
+        } else {
+            c0 = ((wl * P + ll) * NB + wb) * 2;
+            c1 = ((wl * P + ll) * NB + lb) * 2 + 1;
+        }
+        add_split64(lo + c0, hi + c0, q);
+        add_split64(lo + c1, hi + c1, q);
+    }
+    __syncthreads();
+    unsigned long long* st = reinterpret_cast<unsigned long long*>(stats + (size_t)f * cells);
+    for (int k = threadIdx.x; k < cells; k += blockDim.x) {
+        const unsigned long long v = ((unsigned long long)hi[k] << 32) | lo[k];
+        if (v) atomicAdd(st + k, v);
+    }
+}
+
 // The statistics of one level over YetiRank's sampled pairs: a thread per
 // group walks its dense weight matrix (weight qw * cw / perms in f32).
 __global__ void rk_yeti_pairstat_kernel(int n_groups, const int64_t* __restrict__ goff,
@@ -3135,7 +3180,17 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
                 rk_yeti_pairstat_kernel<<<dim3(yg, (unsigned)F), 128, 0, st>>>(
                     s->n_groups, s->d_goff, s->d_cwoff, s->d_cw, s->d_gw, s->yeti_perms, n, leaves, NB, s->bins_fm,
                     s->leaf, s->pw_shift, s->d_pstat);
-            else
+            else if (leaves <= kPsSmemLeaves &&
+                     sizeof(uint32_t) * 2 * (size_t)leaves * leaves * NB * 2 <= (size_t)220 * 1024) {
+                const size_t psm = sizeof(uint32_t) * 2 * (size_t)leaves * leaves * NB * 2;
+                if (psm > 48 * 1024)
+                    MCU(cudaFuncSetAttribute(rk_pairstat_smem_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)psm));
+                // a few shares of the pairs per feature: each block flushes its whole table
+                const unsigned shares = (unsigned)std::max<int64_t>(1, std::min<int64_t>(4, s->n_pairs >> 20));
+                rk_pairstat_smem_kernel<<<dim3(shares, (unsigned)F), kPsThreads, psm, st>>>(
+                    s->n_pairs, n, leaves, NB, s->d_pwin, s->d_closer, s->bins_fm, s->leaf, s->pw_shift, s->d_pstat);
+            } else
                 rk_pairstat_kernel<<<dim3(grid_for(s->n_pairs), (unsigned)F), kMcThreads, 0, st>>>(
                     s->n_pairs, n, leaves, NB, s->d_pwin, s->d_closer, s->bins_fm, s->leaf, s->pw_shift, s->d_pstat);
             rk_pairprefix_kernel<<<grid_for(rows), kMcThreads, 0, st>>>(rows, NB, s->d_pstat);
