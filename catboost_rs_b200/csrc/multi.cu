@@ -1721,18 +1721,22 @@ __device__ __forceinline__ void pw_stat_pair(int wb, int lb, int wl, int ll, int
     }
 }
 
-// The statistics of one level over an explicit pair list of unit weight.
+// The statistics of one level over a pair list: explicit pairs of unit weight
+// (pq null), or YetiRank's compacted samples with their fixed-point weights
+// pq and their count in n_dev (n_pairs then bounds it).
 __global__ void rk_pairstat_kernel(int64_t n_pairs, int64_t n, int P, int NB, const int64_t* __restrict__ pw,
                                    const int64_t* __restrict__ pl, const uint8_t* __restrict__ bins_fm,
-                                   const uint16_t* __restrict__ leaf, int pw_shift, long long* __restrict__ stats) {
+                                   const uint16_t* __restrict__ leaf, int pw_shift, long long* __restrict__ stats,
+                                   const long long* __restrict__ pq, const unsigned long long* __restrict__ n_dev) {
     const int f = blockIdx.y;
     const uint8_t* col = bins_fm + (size_t)f * (size_t)n;
     long long* st = stats + (size_t)f * P * P * NB * 2;
     const long long unit = 1ll << pw_shift;
-    for (int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < n_pairs; k += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t np = n_dev ? (int64_t)min(*n_dev, (unsigned long long)n_pairs) : n_pairs;
+    for (int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < np; k += (int64_t)gridDim.x * blockDim.x) {
         const int64_t w = pw[k], l = pl[k];
         if (w == l) continue;
-        pw_stat_pair(col[w], col[l], leaf[w], leaf[l], P, NB, unit, st);
+        pw_stat_pair(col[w], col[l], leaf[w], leaf[l], P, NB, pq ? pq[k] : unit, st);
     }
 }
 
@@ -1747,7 +1751,7 @@ constexpr int kPsThreads = 1024;
 __global__ void __launch_bounds__(kPsThreads) rk_pairstat_smem_kernel(
     int64_t n_pairs, int64_t n, int P, int NB, const int64_t* __restrict__ pw, const int64_t* __restrict__ pl,
     const uint8_t* __restrict__ bins_fm, const uint16_t* __restrict__ leaf, int pw_shift,
-    long long* __restrict__ stats) {
+    long long* __restrict__ stats, const long long* __restrict__ pq, const unsigned long long* __restrict__ n_dev) {
     extern __shared__ uint32_t pst[];  // lo words [cells], then hi words [cells]
     const int f = blockIdx.y;
     const uint8_t* col = bins_fm + (size_t)f * (size_t)n;
@@ -1756,10 +1760,12 @@ __global__ void __launch_bounds__(kPsThreads) rk_pairstat_smem_kernel(
     uint32_t* hi = pst + cells;
     for (int k = threadIdx.x; k < 2 * cells; k += blockDim.x) pst[k] = 0u;
     __syncthreads();
-    const long long q = -(1ll << pw_shift);
-    for (int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < n_pairs; k += (int64_t)gridDim.x * blockDim.x) {
+    const long long unit = -(1ll << pw_shift);
+    const int64_t np = n_dev ? (int64_t)min(*n_dev, (unsigned long long)n_pairs) : n_pairs;
+    for (int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < np; k += (int64_t)gridDim.x * blockDim.x) {
         const int64_t w = pw[k], l = pl[k];
         if (w == l) continue;
+        const long long q = pq ? -pq[k] : unit;
         const int wb = col[w], lb = col[l], wl = leaf[w], ll = leaf[l];
         if (wl >= P || ll >= P || wb >= NB || lb >= NB) continue;
         int c0, c1;  // pw_stat_pair's two cells
@@ -1781,28 +1787,53 @@ __global__ void __launch_bounds__(kPsThreads) rk_pairstat_smem_kernel(
     }
 }
 
-// The statistics of one level over YetiRank's sampled pairs: a thread per
-// group walks its dense weight matrix (weight qw * cw / perms in f32).
-__global__ void rk_yeti_pairstat_kernel(int n_groups, const int64_t* __restrict__ goff,
-                                        const int64_t* __restrict__ cwoff, const float* __restrict__ cw,
-                                        const double* __restrict__ gw, int perms, int64_t n, int P, int NB,
-                                        const uint8_t* __restrict__ bins_fm, const uint16_t* __restrict__ leaf,
-                                        int pw_shift, long long* __restrict__ stats) {
-    const int gi = blockIdx.x * blockDim.x + threadIdx.x;
-    if (gi >= n_groups) return;
-    const int f = blockIdx.y;
-    const uint8_t* col = bins_fm + (size_t)f * (size_t)n;
-    long long* st = stats + (size_t)f * P * P * NB * 2;
+// YetiRank's sampled pairs as a list, once per resample: a warp per group
+// walks its dense matrix and appends every cell that is a pair of the
+// pairwise statistics (weight wf = qw * cw / perms in f32, non-zero, winner
+// != loser; compute_pair_weight_statistics, pairwise_scoring.rs:163-198)
+// with its fixed-point weight llrint(wf * 2^pw_shift); the level kernels then
+// take the list like explicit pairs.  List order does not matter: the statistics are
+// integer sums.  A list longer than cap (possible only with a non-finite
+// group weight) is cut and flagged.
+__global__ void __launch_bounds__(kYetiWarps * 32) rk_yeti_compact_kernel(
+    int n_groups, const int64_t* __restrict__ goff, const int64_t* __restrict__ cwoff, const float* __restrict__ cw,
+    const double* __restrict__ gw, int perms, int pw_shift, int64_t cap, int64_t* __restrict__ out_w,
+    int64_t* __restrict__ out_l, long long* __restrict__ out_q, unsigned long long* __restrict__ count,
+    McState* __restrict__ ms) {
+    const int lane = threadIdx.x & 31;
+    const int gi = blockIdx.x * kYetiWarps + (threadIdx.x >> 5);
+    if (gi >= n_groups) return;  // warp-uniform
     const int64_t b = goff[gi], g = goff[gi + 1] - b;
     const float* cwg = cw + cwoff[gi];
     const float qw = __double2float_rn(gw[gi]), den = (float)perms;
-    for (int64_t wl = 0; wl < g; ++wl)
-        for (int64_t ll = 0; ll < g; ++ll) {
-            const float wf = __fdiv_rn(__fmul_rn(qw, cwg[wl * g + ll]), den);
-            if (wf == 0.0f || wl == ll) continue;
-            const long long q = llrint(ldexp((double)wf, pw_shift));
-            pw_stat_pair(col[b + wl], col[b + ll], leaf[b + wl], leaf[b + ll], P, NB, q, st);
+    for (int64_t c0 = 0; c0 < g * g; c0 += 32) {
+        const int64_t c = c0 + lane;
+        bool keep = false;
+        long long q = 0;
+        int64_t wl = 0, ll = 0;
+        if (c < g * g) {
+            wl = c / g;
+            ll = c - wl * g;
+            const float wf = __fdiv_rn(__fmul_rn(qw, cwg[c]), den);
+            keep = !(wf == 0.0f || wl == ll);
+            if (keep) q = llrint(ldexp((double)wf, pw_shift));
         }
+        const unsigned m = __ballot_sync(0xffffffffu, keep);
+        if (!m) continue;
+        unsigned long long base = 0;
+        if (lane == 0) base = atomicAdd(count, (unsigned long long)__popc(m));
+        base = __shfl_sync(0xffffffffu, base, 0);
+        if (keep) {
+            const unsigned long long at = base + (unsigned long long)__popc(m & ((1u << lane) - 1u));
+            if (at < (unsigned long long)cap) {
+                out_w[at] = b + wl;
+                out_l[at] = b + ll;
+                out_q[at] = q;
+            } else {
+                atomicOr(&ms->err, kMcErrNonFinite);
+            }
+        }
+    }
 }
 
 // Inclusive prefix over bins of every (feature, leaf, leaf, kind) row.
@@ -2148,6 +2179,11 @@ struct cbgpu_multi_session {
     int64_t *d_lstart = nullptr, *d_lpair = nullptr;
     double* d_pex = nullptr;
     double* d_pairw = nullptr;  // [n_pairs] pair weight per competitor slot (closer order)
+    // YetiRankPairwise: the tree's sampled pairs as a list (rk_yeti_compact_kernel)
+    int64_t *d_ypw = nullptr, *d_ypl = nullptr;
+    long long* d_ypq = nullptr;
+    unsigned long long* d_ypn = nullptr;
+    int64_t ycap = 0;
     long long *d_pstat = nullptr, *d_pwsum = nullptr;
     int pw_shift = 0;  // pair weights in the statistics: llrint(w * 2^pw_shift)
     double* d_pwscratch = nullptr;
@@ -2210,6 +2246,10 @@ struct cbgpu_multi_session {
         cudaFree(d_lpair);
         cudaFree(d_pex);
         cudaFree(d_pairw);
+        cudaFree(d_ypw);
+        cudaFree(d_ypl);
+        cudaFree(d_ypq);
+        cudaFree(d_ypn);
         cudaFree(d_pstat);
         cudaFree(d_pwsum);
         cudaFree(d_pwscratch);
@@ -2780,6 +2820,14 @@ int cbgpu_rank_begin_raw(const cbgpu_begin_args* a, const int64_t* group_offsets
             if (!rc) rc = mhalloc(&s->h_yseeds, 3 * (size_t)n_groups);
             if (!rc) rc = mdalloc(&s->d_cwoff, (size_t)n_groups);
             if (!rc) rc = mdalloc(&s->d_cw, (size_t)std::max<int64_t>(cells, 1));
+            if (!rc && mode == kRankYetiRankPairwise) {
+                // a permutation adds at most g - 1 cells per group: perms * n bounds the list
+                s->ycap = std::max<int64_t>(1, std::min<int64_t>(cells, (int64_t)std::max(yeti_perms, 1) * n));
+                rc = mdalloc(&s->d_ypw, (size_t)s->ycap);
+                if (!rc) rc = mdalloc(&s->d_ypl, (size_t)s->ycap);
+                if (!rc) rc = mdalloc(&s->d_ypq, (size_t)s->ycap);
+                if (!rc) rc = mdalloc(&s->d_ypn, 1);
+            }
             if (!rc) rc = mdalloc(&s->d_lmorder, (size_t)n);
             if (!rc) rc = mdalloc(&s->d_yboot, (size_t)n);
             if (!rc) {
@@ -3067,6 +3115,12 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
                                                  s->d_yboot);
         rk_yeti_der_kernel<<<yw, kYetiWarps * 32, 0, st>>>(s->n_groups, s->d_goff, s->d_lapprox, s->d_gw, s->yeti_perms,
                                               s->d_cwoff, s->d_cw, s->wd1, s->d_der2, s->d_eff, s->d_yboot, s->d_ms);
+        if (s->rank_mode == kRankYetiRankPairwise) {  // the split search's pairs, as a list
+            MCU(cudaMemsetAsync(s->d_ypn, 0, sizeof(unsigned long long), st));
+            rk_yeti_compact_kernel<<<yw, kYetiWarps * 32, 0, st>>>(s->n_groups, s->d_goff, s->d_cwoff, s->d_cw,
+                                                                   s->d_gw, s->yeti_perms, s->pw_shift, s->ycap,
+                                                                   s->d_ypw, s->d_ypl, s->d_ypq, s->d_ypn, s->d_ms);
+        }
     } else if (srank) {
         rk_srank_kernel<<<yg, 128, 0, st>>>(s->n_groups, s->d_goff, s->approx, s->d_tgt, s->srank_ndcg, s->srank_sigma,
                                            s->srank_mu, s->srank_num_est, srank_base[0], s->d_lmden, s->d_lmideal,
@@ -3176,23 +3230,26 @@ int cbgpu_multi_grow_tree(cbgpu_multi_session* s, const double* approx_k, const 
         if (pairwise) {
             const int64_t rows = (int64_t)F * leaves * leaves * 2;
             MCU(cudaMemsetAsync(s->d_pstat, 0, sizeof(long long) * (size_t)rows * NB, st));
-            if (yeti)
-                rk_yeti_pairstat_kernel<<<dim3(yg, (unsigned)F), 128, 0, st>>>(
-                    s->n_groups, s->d_goff, s->d_cwoff, s->d_cw, s->d_gw, s->yeti_perms, n, leaves, NB, s->bins_fm,
-                    s->leaf, s->pw_shift, s->d_pstat);
-            else if (leaves <= kPsSmemLeaves &&
-                     sizeof(uint32_t) * 2 * (size_t)leaves * leaves * NB * 2 <= (size_t)220 * 1024) {
-                const size_t psm = sizeof(uint32_t) * 2 * (size_t)leaves * leaves * NB * 2;
+            // YetiRankPairwise: the tree's compacted samples with their
+            // weights; PairLogitPairwise: the explicit pairs, unit weights
+            const int64_t* PW = yeti ? s->d_ypw : s->d_pwin;
+            const int64_t* PL = yeti ? s->d_ypl : s->d_closer;
+            const long long* PQ = yeti ? s->d_ypq : nullptr;
+            const unsigned long long* ND = yeti ? s->d_ypn : nullptr;
+            const int64_t NP = yeti ? s->ycap : s->n_pairs;
+            const size_t psm = sizeof(uint32_t) * 2 * (size_t)leaves * leaves * NB * 2;
+            if (leaves <= kPsSmemLeaves && psm <= (size_t)220 * 1024) {
                 if (psm > 48 * 1024)
                     MCU(cudaFuncSetAttribute(rk_pairstat_smem_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)psm));
                 // a few shares of the pairs per feature: each block flushes its whole table
-                const unsigned shares = (unsigned)std::max<int64_t>(1, std::min<int64_t>(4, s->n_pairs >> 20));
+                const unsigned shares = (unsigned)std::max<int64_t>(1, std::min<int64_t>(4, NP >> 20));
                 rk_pairstat_smem_kernel<<<dim3(shares, (unsigned)F), kPsThreads, psm, st>>>(
-                    s->n_pairs, n, leaves, NB, s->d_pwin, s->d_closer, s->bins_fm, s->leaf, s->pw_shift, s->d_pstat);
-            } else
-                rk_pairstat_kernel<<<dim3(grid_for(s->n_pairs), (unsigned)F), kMcThreads, 0, st>>>(
-                    s->n_pairs, n, leaves, NB, s->d_pwin, s->d_closer, s->bins_fm, s->leaf, s->pw_shift, s->d_pstat);
+                    NP, n, leaves, NB, PW, PL, s->bins_fm, s->leaf, s->pw_shift, s->d_pstat, PQ, ND);
+            } else {
+                rk_pairstat_kernel<<<dim3(grid_for(NP), (unsigned)F), kMcThreads, 0, st>>>(
+                    NP, n, leaves, NB, PW, PL, s->bins_fm, s->leaf, s->pw_shift, s->d_pstat, PQ, ND);
+            }
             rk_pairprefix_kernel<<<grid_for(rows), kMcThreads, 0, st>>>(rows, NB, s->d_pstat);
             const int n2 = 2 * leaves;
             const int pw_smem = n2 <= kPwSmemMaxN2 ? 1 : 0;
